@@ -1,0 +1,213 @@
+"""Typed configuration for the engine: model shape, parallel layout, quantisation and kernel flags.
+
+One dataclass tree drives the CPU fp32 oracle (``carbon_b200.ref``), the GPU model (``carbon_b200.models``) and the
+serving engine (``carbon_b200.engine``).  The reference keeps these facts as module constants and domain checks
+(``king_v10/bundle_v9/slots.py:133-158`` checks 40 layers / hidden 5120 / 384 experts / top-6; ``moe_front.py:17``
+etc.); here every one of them is a field so that the DeepSeek-V3 shape (61 layers, hidden 7168, 256 experts top-8)
+and the V4.1-Flash shape are both expressible.
+
+Overrides: ``ModelConfig.from_dict`` / ``from_yaml`` and ``CARBON_<FIELD>=value`` environment variables
+(``apply_env``), mirroring the reference's module-level switches (``EVL_ON``, ``WTILE`` …) with one typed mechanism.
+"""
+from __future__ import annotations
+
+import dataclasses
+import json
+import os
+from dataclasses import dataclass, field
+from typing import Any, Dict, Optional
+
+
+@dataclass
+class ModelConfig:
+    """Shape of a DeepSeek-V3/V4-style transformer: MLA + DSA indexer + fine-grained MoE + mHC."""
+
+    vocab_size: int = 129280
+    hidden_size: int = 7168
+    n_layers: int = 61
+    n_dense_layers: int = 3            # first layers use a dense SwiGLU FFN instead of MoE
+    dense_intermediate: int = 18432
+    # MLA attention
+    n_heads: int = 128
+    q_lora_rank: int = 1536            # 0 => q projected directly from hidden
+    kv_lora_rank: int = 512
+    qk_nope_head_dim: int = 128
+    qk_rope_head_dim: int = 64
+    v_head_dim: int = 128
+    rope_theta: float = 10000.0
+    max_position: int = 16384
+    # DSA lightning indexer (0 heads => dense attention)
+    index_n_heads: int = 64
+    index_head_dim: int = 128
+    index_topk: int = 2048
+    # MoE
+    n_routed_experts: int = 256
+    n_activated_experts: int = 8
+    n_shared_experts: int = 1
+    moe_intermediate: int = 2048
+    score_func: str = "sigmoid"        # sigmoid | sqrtsoftplus | softmax
+    route_scale: float = 2.5
+    norm_topk_prob: bool = True
+    swiglu_limit: float = 0.0          # 0 => no clamp
+    # mHC (manifold-constrained hyper-connections)
+    hc_mult: int = 4
+    sinkhorn_iters: int = 20
+    hc_eps: float = 1e-6
+    rms_eps: float = 1e-6
+    init_std: float = 0.02
+    tie_word_embeddings: bool = False
+
+    # ---- derived -------------------------------------------------------------------------------------------------
+    @property
+    def qk_head_dim(self) -> int:
+        return self.qk_nope_head_dim + self.qk_rope_head_dim
+
+    @property
+    def hc_mix_dim(self) -> int:
+        """Number of mHC mixing outputs: hc pre + hc post + hc×hc comb."""
+        return 2 * self.hc_mult + self.hc_mult * self.hc_mult
+
+    @property
+    def use_indexer(self) -> bool:
+        return self.index_n_heads > 0 and self.index_topk > 0
+
+    def is_moe_layer(self, layer: int) -> bool:
+        return layer >= self.n_dense_layers and self.n_routed_experts > 0
+
+    @property
+    def softmax_scale(self) -> float:
+        return self.qk_head_dim ** -0.5
+
+    # ---- construction --------------------------------------------------------------------------------------------
+    @classmethod
+    def from_dict(cls, d: Dict[str, Any]) -> "ModelConfig":
+        names = {f.name for f in dataclasses.fields(cls)}
+        unknown = set(d) - names
+        if unknown:
+            raise ValueError(f"unknown ModelConfig fields: {sorted(unknown)}")
+        return cls(**d)
+
+    @classmethod
+    def from_yaml(cls, path: str) -> "ModelConfig":
+        import yaml
+
+        with open(path) as f:
+            return cls.from_dict(yaml.safe_load(f) or {})
+
+    def to_dict(self) -> Dict[str, Any]:
+        return dataclasses.asdict(self)
+
+    def replace(self, **kw) -> "ModelConfig":
+        return dataclasses.replace(self, **kw)
+
+    def validate(self) -> None:
+        assert self.hidden_size % 128 == 0 or self.hidden_size < 128, "hidden must be a multiple of 128 (fp8 1x128 blocks)"
+        assert self.qk_rope_head_dim % 2 == 0
+        assert self.n_activated_experts <= max(self.n_routed_experts, 1)
+        assert self.score_func in ("sigmoid", "sqrtsoftplus", "softmax")
+        if self.use_indexer:
+            assert self.index_head_dim >= self.qk_rope_head_dim
+
+
+def tiny_config() -> ModelConfig:
+    """the tiny CPU model (2 layers, hidden 256, vocab 1024)."""
+    return ModelConfig(
+        vocab_size=1024, hidden_size=256, n_layers=2, n_dense_layers=0, dense_intermediate=512,
+        n_heads=4, q_lora_rank=128, kv_lora_rank=64, qk_nope_head_dim=32, qk_rope_head_dim=16, v_head_dim=32,
+        max_position=1024,
+        index_n_heads=2, index_head_dim=32, index_topk=32,
+        n_routed_experts=8, n_activated_experts=2, n_shared_experts=1, moe_intermediate=128,
+        score_func="sigmoid", route_scale=1.0,
+        hc_mult=4, sinkhorn_iters=20, rms_eps=1e-6,
+    )
+
+
+def deepseek_v3_config() -> ModelConfig:
+    """the full-size DeepSeek-V3/V4-class model (61 layers, hidden 7168, 256 experts top-8)."""
+    return ModelConfig()
+
+
+def small_gpu_config() -> ModelConfig:
+    """A 4-layer slice at reduced width that keeps every full-size kernel constraint (multiples of 128)."""
+    return ModelConfig(
+        vocab_size=8192, hidden_size=1024, n_layers=4, n_dense_layers=1, dense_intermediate=2048,
+        n_heads=16, q_lora_rank=512, kv_lora_rank=512, qk_nope_head_dim=128, qk_rope_head_dim=64, v_head_dim=128,
+        max_position=8192, index_n_heads=8, index_head_dim=128, index_topk=256,
+        n_routed_experts=32, n_activated_experts=4, n_shared_experts=1, moe_intermediate=256,
+        route_scale=2.5,
+    )
+
+
+PRESETS = {"tiny": tiny_config, "deepseek_v3": deepseek_v3_config, "small": small_gpu_config}
+
+
+@dataclass
+class ParallelConfig:
+    """Parallel layout on one node: tensor-parallel attention, expert-parallel MoE, DP-attention."""
+
+    world_size: int = 1
+    rank: int = 0
+    tp: int = 1                  # attention tensor parallel (heads split)
+    ep: int = 1                  # expert parallel (experts split)
+    dp_attention: bool = False   # attention data-parallel (each rank its own requests), MoE EP
+    vocab_parallel: bool = True  # embedding / LM head split over ranks, served from peer HBM
+
+    def validate(self, cfg: ModelConfig) -> None:
+        assert self.world_size >= 1
+        if self.tp > 1:
+            assert cfg.n_heads % self.tp == 0, "heads must divide TP"
+        if self.ep > 1:
+            assert cfg.n_routed_experts % self.ep == 0, "experts must divide EP"
+
+
+@dataclass
+class KernelFlags:
+    """Per-path switches (the reference's lever constants, as one typed record)."""
+
+    fused_ep_moe: bool = True       # in-kernel NVLink dispatch/combine (else NCCL all-to-all baseline)
+    fused_tp_attn: bool = True      # o_proj GEMM -> reduce-scatter over peer memory (else NCCL)
+    peer_vocab: bool = True         # embedding / LM head from peer HBM (else NCCL all-gather)
+    cuda_graphs: bool = True        # capture decode steps
+    fp8_gemm: bool = True           # block-scaled fp8 GEMMs (else bf16)
+    sparse_attention: bool = True   # DSA top-k attention when the model has an indexer
+
+    @classmethod
+    def from_env(cls) -> "KernelFlags":
+        f = cls()
+        apply_env(f, prefix="CARBON_")
+        return f
+
+
+@dataclass
+class EngineConfig:
+    model: ModelConfig = field(default_factory=ModelConfig)
+    parallel: ParallelConfig = field(default_factory=ParallelConfig)
+    flags: KernelFlags = field(default_factory=KernelFlags)
+    kv_page_size: int = 64
+    max_batch: int = 256
+    max_seq_len: int = 8192
+    decode_graph_buckets: tuple = (1, 2, 4, 8, 16, 32, 64, 128, 256)
+    seed: int = 0
+    weight_layer_sets: Optional[int] = None  # None => one weight set per layer
+
+
+def _coerce(val: str, typ):
+    if typ in (bool, "bool"):
+        return val.lower() in ("1", "true", "yes", "on")
+    if typ in (int, "int"):
+        return int(val)
+    if typ in (float, "float"):
+        return float(val)
+    return val
+
+
+def apply_env(obj, prefix: str = "CARBON_") -> None:
+    """Override dataclass fields from ``<prefix><FIELD_NAME_UPPER>`` environment variables."""
+    for f in dataclasses.fields(obj):
+        key = prefix + f.name.upper()
+        if key in os.environ:
+            setattr(obj, f.name, _coerce(os.environ[key], f.type))
+
+
+def dump(obj) -> str:
+    return json.dumps(dataclasses.asdict(obj), sort_keys=True)

@@ -1,0 +1,233 @@
+// Python bindings of the CUDA kernels. Shape / dtype / device checks live here; kernels take raw pointers.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include "small_ops.h"
+
+namespace {
+
+#define CHECK_CUDA(t) TORCH_CHECK((t).is_cuda(), #t " must be a CUDA tensor")
+#define CHECK_CONTIG(t) TORCH_CHECK((t).is_contiguous(), #t " must be contiguous")
+#define CHECK_DT(t, d) TORCH_CHECK((t).scalar_type() == (d), #t " has dtype ", (t).scalar_type(), ", expected ", (d))
+#define CK(expr)                                                                          \
+  do {                                                                                    \
+    cudaError_t _e = (expr);                                                              \
+    TORCH_CHECK(_e == cudaSuccess, #expr " failed: ", cudaGetErrorString(_e));            \
+  } while (0)
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <typename T>
+T* ptr_or_null(const c10::optional<torch::Tensor>& t) {
+  return t.has_value() && t->defined() ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+
+int64_t sf_words(int64_t M, int64_t K) { return ((K + 511) / 512) * ((M + 127) / 128) * 128; }
+
+// ---------------------------------------------------------------------------------------------------------------
+void act_quant(torch::Tensor x, torch::Tensor q, torch::Tensor sf, c10::optional<torch::Tensor> src_rows, int64_t M) {
+  CHECK_CUDA(x); CHECK_DT(x, at::kBFloat16); CHECK_DT(q, at::kFloat8_e4m3fn); CHECK_DT(sf, at::kInt);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1);
+  const int K = x.size(1);
+  TORCH_CHECK(q.size(0) >= M && q.size(1) == K && q.is_contiguous());
+  TORCH_CHECK(sf.numel() >= sf_words(M, K));
+  if (!src_rows.has_value()) TORCH_CHECK(x.size(0) >= M);
+  c10::cuda::CUDAGuard g(x.device());
+  CK(cb::act_quant(x.data_ptr(), x.stride(0), q.data_ptr(), K, reinterpret_cast<uint32_t*>(sf.data_ptr()), M, K,
+                   ptr_or_null<const int>(src_rows), cur_stream()));
+}
+
+void rms_norm(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> y, c10::optional<torch::Tensor> q,
+              c10::optional<torch::Tensor> sf, double eps) {
+  CHECK_CUDA(x); CHECK_DT(x, at::kBFloat16); CHECK_DT(w, at::kFloat);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1);
+  const int M = x.size(0), D = x.size(1);
+  int ldy = D;
+  if (y.has_value()) { CHECK_DT((*y), at::kBFloat16); TORCH_CHECK(y->stride(1) == 1); ldy = y->stride(0); }
+  if (q.has_value()) { TORCH_CHECK(sf.has_value()); TORCH_CHECK(sf->numel() >= sf_words(M, D)); }
+  c10::cuda::CUDAGuard g(x.device());
+  CK(cb::rms_norm(x.data_ptr(), x.stride(0), w.data_ptr<float>(), ptr_or_null<void>(y), ldy, ptr_or_null<void>(q),
+                  ptr_or_null<uint32_t>(sf), M, D, float(eps), cur_stream()));
+  if (q.has_value()) CK(cb::sf_pad(reinterpret_cast<uint32_t*>(sf->data_ptr()), M, D, cur_stream()));
+}
+
+void rope(torch::Tensor x, int64_t off, int64_t dim, torch::Tensor cos_sin, torch::Tensor pos, bool inverse) {
+  CHECK_CUDA(x); CHECK_DT(x, at::kBFloat16); CHECK_DT(cos_sin, at::kFloat); CHECK_DT(pos, at::kInt);
+  TORCH_CHECK(x.dim() == 3 && x.stride(2) == 1, "rope expects [T, H, d] with unit inner stride");
+  TORCH_CHECK(cos_sin.size(1) == dim);
+  c10::cuda::CUDAGuard g(x.device());
+  CK(cb::rope_inplace(x.data_ptr(), x.size(0), x.stride(0), x.stride(1), x.size(1), off, dim,
+                      cos_sin.data_ptr<float>(), pos.data_ptr<int>(), inverse, cur_stream()));
+}
+
+void router_topk(torch::Tensor logits, c10::optional<torch::Tensor> bias, int64_t k, int64_t score, bool norm,
+                 double route_scale, torch::Tensor w, torch::Tensor ids) {
+  CHECK_CUDA(logits); CHECK_DT(logits, at::kFloat); CHECK_CONTIG(logits);
+  CHECK_DT(w, at::kFloat); CHECK_DT(ids, at::kInt);
+  c10::cuda::CUDAGuard g(logits.device());
+  CK(cb::router_topk(logits.data_ptr<float>(), ptr_or_null<const float>(bias), logits.size(0), logits.size(1), k,
+                     score, norm, float(route_scale), w.data_ptr<float>(), ids.data_ptr<int>(), cur_stream()));
+}
+
+void moe_layout(torch::Tensor ids, int64_t E, torch::Tensor slot_pos, torch::Tensor row_src,
+                torch::Tensor m_block_expert, torch::Tensor num_blocks, c10::optional<torch::Tensor> counts) {
+  CHECK_CUDA(ids); CHECK_DT(ids, at::kInt); CHECK_CONTIG(ids);
+  TORCH_CHECK(row_src.numel() >= m_block_expert.numel() * 128);
+  c10::cuda::CUDAGuard g(ids.device());
+  CK(cb::moe_layout(ids.data_ptr<int>(), ids.size(0), ids.size(1), E, m_block_expert.numel(),
+                    slot_pos.data_ptr<int>(), row_src.data_ptr<int>(), m_block_expert.data_ptr<int>(),
+                    num_blocks.data_ptr<int>(), ptr_or_null<int>(counts), cur_stream()));
+}
+
+void moe_combine(torch::Tensor Y, torch::Tensor w, torch::Tensor slot_pos, c10::optional<torch::Tensor> add,
+                 torch::Tensor out) {
+  CHECK_CUDA(Y); CHECK_DT(Y, at::kBFloat16); CHECK_DT(out, at::kBFloat16); CHECK_CONTIG(out);
+  TORCH_CHECK(Y.stride(1) == 1);
+  c10::cuda::CUDAGuard g(Y.device());
+  CK(cb::moe_combine(Y.data_ptr(), Y.stride(0), w.data_ptr<float>(), slot_pos.data_ptr<int>(), out.size(0),
+                     slot_pos.size(1), ptr_or_null<const void>(add), out.data_ptr(), out.size(1), cur_stream()));
+}
+
+void mhc_coeffs(torch::Tensor mix, torch::Tensor sumsq, torch::Tensor base, torch::Tensor scale, int64_t flat_dim,
+                int64_t iters, double hc_eps, double rms_eps, torch::Tensor pre, torch::Tensor post,
+                torch::Tensor comb) {
+  CHECK_CUDA(mix); CHECK_DT(mix, at::kFloat);
+  TORCH_CHECK(mix.size(1) >= 48 && mix.stride(1) == 1);
+  c10::cuda::CUDAGuard g(mix.device());
+  CK(cb::mhc_coeffs(mix.data_ptr<float>(), mix.stride(0), sumsq.data_ptr<float>(), base.data_ptr<float>(),
+                    scale.data_ptr<float>(), mix.size(0), flat_dim, iters, hc_eps, rms_eps, pre.data_ptr<float>(),
+                    post.data_ptr<float>(), comb.data_ptr<float>(), cur_stream()));
+}
+
+void mhc_head_coeffs(torch::Tensor mix, torch::Tensor sumsq, torch::Tensor base, torch::Tensor scale,
+                     int64_t flat_dim, double hc_eps, double rms_eps, torch::Tensor pre) {
+  CHECK_CUDA(mix); CHECK_DT(mix, at::kFloat);
+  c10::cuda::CUDAGuard g(mix.device());
+  CK(cb::mhc_head_coeffs(mix.data_ptr<float>(), mix.stride(0), sumsq.data_ptr<float>(), base.data_ptr<float>(),
+                         scale.data_ptr<float>(), mix.size(0), flat_dim, hc_eps, rms_eps, pre.data_ptr<float>(),
+                         cur_stream()));
+}
+
+void mhc_pre_norm(torch::Tensor X, torch::Tensor pre, torch::Tensor w, double eps, c10::optional<torch::Tensor> y,
+                  c10::optional<torch::Tensor> q, c10::optional<torch::Tensor> sf, c10::optional<torch::Tensor> rows) {
+  CHECK_CUDA(X); CHECK_DT(X, at::kBFloat16); CHECK_CONTIG(X);
+  TORCH_CHECK(X.dim() == 3 && X.size(1) == 4);
+  const int T = rows.has_value() ? rows->numel() : X.size(0);
+  const int D = X.size(2);
+  if (q.has_value()) { TORCH_CHECK(sf.has_value() && sf->numel() >= sf_words(T, D)); }
+  c10::cuda::CUDAGuard g(X.device());
+  CK(cb::mhc_pre_norm(X.data_ptr(), pre.data_ptr<float>(), w.data_ptr<float>(), T, D, eps, ptr_or_null<void>(y),
+                      ptr_or_null<void>(q), ptr_or_null<uint32_t>(sf), ptr_or_null<const int>(rows), cur_stream()));
+  if (q.has_value()) CK(cb::sf_pad(reinterpret_cast<uint32_t*>(sf->data_ptr()), T, D, cur_stream()));
+}
+
+void mhc_post_mix(torch::Tensor X, torch::Tensor out, torch::Tensor post, torch::Tensor comb, torch::Tensor Xn,
+                  torch::Tensor sumsq) {
+  CHECK_CUDA(X); CHECK_DT(X, at::kBFloat16); CHECK_CONTIG(X); CHECK_CONTIG(out); CHECK_CONTIG(Xn);
+  TORCH_CHECK(X.size(1) == 4);
+  c10::cuda::CUDAGuard g(X.device());
+  CK(cb::mhc_post_mix(X.data_ptr(), out.data_ptr(), post.data_ptr<float>(), comb.data_ptr<float>(), X.size(0),
+                      X.size(2), Xn.data_ptr(), sumsq.data_ptr<float>(), cur_stream()));
+}
+
+void embed_hc(torch::Tensor table, int64_t row_lo, torch::Tensor ids, torch::Tensor X,
+              c10::optional<torch::Tensor> sumsq) {
+  CHECK_CUDA(table); CHECK_DT(table, at::kBFloat16); CHECK_CONTIG(table); CHECK_DT(ids, at::kInt);
+  c10::cuda::CUDAGuard g(table.device());
+  CK(cb::embed_hc(table.data_ptr(), row_lo, table.size(0), ids.data_ptr<int>(), ids.numel(), table.size(1),
+                  X.size(1), X.data_ptr(), ptr_or_null<float>(sumsq), cur_stream()));
+}
+
+void row_sumsq(torch::Tensor x, torch::Tensor out) {
+  CHECK_CUDA(x); CHECK_CONTIG(x); CHECK_DT(x, at::kBFloat16);
+  c10::cuda::CUDAGuard g(x.device());
+  CK(cb::row_sumsq(x.data_ptr(), x.size(0), x.numel() / std::max<int64_t>(x.size(0), 1), out.data_ptr<float>(),
+                   cur_stream()));
+}
+
+void silu_mul(torch::Tensor gu, double limit, torch::Tensor out) {
+  CHECK_CUDA(gu); CHECK_CONTIG(gu); CHECK_CONTIG(out);
+  c10::cuda::CUDAGuard g(gu.device());
+  CK(cb::silu_mul(gu.data_ptr(), gu.size(0), out.size(1), float(limit), out.data_ptr(), cur_stream()));
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// GEMMs
+// ---------------------------------------------------------------------------------------------------------------
+void gemm_fp8(torch::Tensor A, torch::Tensor sfa, torch::Tensor B, torch::Tensor sfb, torch::Tensor out, int64_t epi,
+              c10::optional<torch::Tensor> out_sf, double swiglu_limit, c10::optional<torch::Tensor> m_block_expert,
+              c10::optional<torch::Tensor> num_m_blocks, int64_t N_per_group, c10::optional<torch::Tensor> status) {
+  CHECK_CUDA(A); CHECK_DT(A, at::kFloat8_e4m3fn); CHECK_DT(B, at::kFloat8_e4m3fn); CHECK_CONTIG(A); CHECK_CONTIG(B);
+  CHECK_DT(sfa, at::kInt); CHECK_DT(sfb, at::kInt);
+  const int M = A.size(0), K = A.size(1);
+  const int Nb = B.size(0);
+  TORCH_CHECK(B.size(1) == K, "K mismatch");
+  const bool grouped = m_block_expert.has_value();
+  const int N = grouped ? int(N_per_group) : Nb;
+  TORCH_CHECK(sfa.numel() >= sf_words(M, K), "sfa too small");
+  TORCH_CHECK(sfb.numel() >= sf_words(Nb, K), "sfb too small");
+  TORCH_CHECK(out.stride(-1) == 1);
+  if (epi == cb::GEMM_OUT_SWIGLU_FP8) {
+    CHECK_DT(out, at::kFloat8_e4m3fn);
+    TORCH_CHECK(out_sf.has_value() && out_sf->numel() >= sf_words(M, N / 2));
+  } else if (epi == cb::GEMM_OUT_F32) {
+    CHECK_DT(out, at::kFloat);
+  } else {
+    CHECK_DT(out, at::kBFloat16);
+  }
+  if (grouped) TORCH_CHECK(m_block_expert->numel() * 128 <= M, "grouped rows must cover all m blocks");
+  c10::cuda::CUDAGuard g(A.device());
+  CK(cb::gemm_fp8(A.data_ptr(), B.data_ptr(), reinterpret_cast<uint32_t*>(sfa.data_ptr()),
+                  reinterpret_cast<uint32_t*>(sfb.data_ptr()), M, N, K, Nb, out.data_ptr(), out.stride(0), epi,
+                  ptr_or_null<uint32_t>(out_sf), float(swiglu_limit), ptr_or_null<const int>(m_block_expert),
+                  ptr_or_null<const int>(num_m_blocks), grouped ? m_block_expert->numel() : 0,
+                  ptr_or_null<int>(status), num_sms(), cur_stream()));
+}
+
+void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor out, int64_t epi,
+               c10::optional<torch::Tensor> m_block_expert, c10::optional<torch::Tensor> num_m_blocks,
+               int64_t N_per_group, c10::optional<torch::Tensor> status) {
+  CHECK_CUDA(A); CHECK_DT(A, at::kBFloat16); CHECK_DT(B, at::kBFloat16);
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && out.stride(-1) == 1);
+  const int M = A.size(0), K = A.size(1), Nb = B.size(0);
+  TORCH_CHECK(B.size(1) == K);
+  const bool grouped = m_block_expert.has_value();
+  const int N = grouped ? int(N_per_group) : Nb;
+  if (epi == cb::GEMM_OUT_F32) { CHECK_DT(out, at::kFloat); } else { CHECK_DT(out, at::kBFloat16); }
+  c10::cuda::CUDAGuard g(A.device());
+  CK(cb::gemm_bf16(A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0), M, N, K, Nb, out.data_ptr(), out.stride(0),
+                   epi, ptr_or_null<const int>(m_block_expert), ptr_or_null<const int>(num_m_blocks),
+                   grouped ? m_block_expert->numel() : 0, ptr_or_null<int>(status), num_sms(), cur_stream()));
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "carbon_b200 sm_100a kernels";
+  m.def("act_quant", &act_quant);
+  m.def("rms_norm", &rms_norm);
+  m.def("rope", &rope);
+  m.def("router_topk", &router_topk);
+  m.def("moe_layout", &moe_layout);
+  m.def("moe_combine", &moe_combine);
+  m.def("mhc_coeffs", &mhc_coeffs);
+  m.def("mhc_head_coeffs", &mhc_head_coeffs);
+  m.def("mhc_pre_norm", &mhc_pre_norm);
+  m.def("mhc_post_mix", &mhc_post_mix);
+  m.def("embed_hc", &embed_hc);
+  m.def("row_sumsq", &row_sumsq);
+  m.def("silu_mul", &silu_mul);
+  m.def("gemm_fp8", &gemm_fp8);
+  m.def("gemm_bf16", &gemm_bf16);
+  m.def("sf_words", &sf_words);
+}

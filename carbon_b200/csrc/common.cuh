@@ -1,0 +1,106 @@
+// Common device helpers: types, warp reductions, launch checks, error flags.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#define CB_DEVICE __device__ __forceinline__
+#define CB_HOST_DEVICE __host__ __device__ __forceinline__
+
+#define CB_CUDA_CHECK(expr)                                                                     \
+  do {                                                                                          \
+    cudaError_t _e = (expr);                                                                    \
+    if (_e != cudaSuccess) {                                                                    \
+      fprintf(stderr, "CUDA error %s at %s:%d: %s\n", #expr, __FILE__, __LINE__,                \
+              cudaGetErrorString(_e));                                                          \
+      return _e;                                                                                \
+    }                                                                                           \
+  } while (0)
+
+namespace cb {
+
+constexpr float kFp8Max = 448.0f;
+
+// Error codes written to a device-side status word by kernels whose waits are bounded.
+enum : int {
+  kOk = 0,
+  kErrTimeoutFull = 1,     // producer data never arrived
+  kErrTimeoutEmpty = 2,    // consumer never released a stage
+  kErrTimeoutTmem = 3,     // accumulator hand-off never happened
+  kErrTimeoutPeer = 4,     // a peer rank's flag never arrived
+  kErrBadArg = 5,
+};
+
+CB_DEVICE float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+CB_DEVICE float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block reduction for blockDim.x a multiple of 32 and <= 1024. `smem` holds >= 32 floats.
+CB_DEVICE float block_sum(float v, float* smem) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) smem[wid] = v;
+  __syncthreads();
+  float r = lane < nw ? smem[lane] : 0.f;
+  r = warp_sum(r);
+  return r;
+}
+CB_DEVICE float block_max(float v, float* smem) {
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) smem[wid] = v;
+  __syncthreads();
+  float r = lane < nw ? smem[lane] : -INFINITY;
+  r = warp_max(r);
+  return r;
+}
+
+// Power-of-two scale for an fp8 e4m3 block: smallest 2^e with amax / 2^e <= 448. Returns the biased UE8M0 byte
+// (e + 127). Computed exactly from the fp32 exponent bits; no transcendental functions are involved.
+CB_DEVICE uint32_t ue8m0_for_amax(float amax) {
+  if (!(amax > 0.f)) return 127u;  // scale 1.0 for all-zero blocks
+  float r = amax / kFp8Max;        // want smallest e with 2^e >= r
+  uint32_t bits = __float_as_uint(r);
+  int e = int((bits >> 23) & 0xff) - 127;
+  if (bits & 0x7fffff) e += 1;     // not an exact power of two: round the exponent up
+  int biased = e + 127;
+  biased = biased < 1 ? 1 : (biased > 254 ? 254 : biased);
+  return uint32_t(biased);
+}
+CB_DEVICE float ue8m0_to_float(uint32_t b) { return __uint_as_float(b << 23); }
+// 1 / scale, exact for powers of two.
+CB_DEVICE float ue8m0_inv(uint32_t b) { return __uint_as_float((254u - b) << 23); }
+
+CB_DEVICE __nv_bfloat162 f2_to_bf2(float a, float b) { return __floats2bfloat162_rn(a, b); }
+
+CB_DEVICE uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// Pack 4 floats (already scaled into e4m3 range) into 4 fp8 e4m3 bytes (satfinite, round-to-nearest-even).
+CB_DEVICE uint32_t pack_fp8x4(float a, float b, float c, float d) {
+  __nv_fp8x2_e4m3 lo(make_float2(a, b));
+  __nv_fp8x2_e4m3 hi(make_float2(c, d));
+  return uint32_t(*reinterpret_cast<uint16_t*>(&lo)) | (uint32_t(*reinterpret_cast<uint16_t*>(&hi)) << 16);
+}
+
+CB_DEVICE float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
+CB_DEVICE float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+
+CB_HOST_DEVICE int ceil_div(int a, int b) { return (a + b - 1) / b; }
+CB_HOST_DEVICE int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+}  // namespace cb

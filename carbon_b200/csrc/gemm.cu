@@ -1,0 +1,105 @@
+// Host side of the tcgen05 GEMMs: TMA tensor-map encoding, instantiation choice, launch.
+#include <cudaTypedefs.h>
+#include <mutex>
+#include "gemm.cuh"
+#include "small_ops.h"
+
+namespace cb {
+
+static PFN_cuTensorMapEncodeTiled_v12000 tmap_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D K-major tile map: [rows, inner] with 128-byte swizzled boxes of (box_inner x box_rows).
+bool make_tmap_2d(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+                  uint64_t rows, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows,
+                  CUtensorMapSwizzle swz) {
+  auto fn = tmap_encode_fn();
+  if (!fn) return false;
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || (row_stride_bytes & 15)) return false;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, dt, 2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  (void)elem_bytes;
+  return r == CUDA_SUCCESS;
+}
+
+template <int KIND, int EPI, int BN, int ST, int ACC>
+static cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int max_tiles,
+                          int num_sms, cudaStream_t s) {
+  constexpr int smem = gemm_smem_bytes<KIND, BN, ST>();
+  auto kern = gemm_tc_kernel<KIND, EPI, BN, ST, ACC>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    attr_set = true;
+  }
+  const int grid = max_tiles < num_sms ? max_tiles : num_sms;
+  if (grid <= 0) return cudaSuccess;
+  kern<<<grid, 256, smem, s>>>(ta, tb, p);
+  return cudaGetLastError();
+}
+
+cudaError_t gemm_fp8(const void* A, const void* B, const uint32_t* sfa, const uint32_t* sfb, int M, int N, int K,
+                     int Nb, void* out, int ldo, int epi, uint32_t* out_sf, float swiglu_limit,
+                     const int* m_block_expert, const int* num_m_blocks_dev, int max_m_blocks, int* status,
+                     int num_sms, cudaStream_t s) {
+  if (M <= 0 || N <= 0) return cudaSuccess;
+  if (K % 128 || N % 16) return cudaErrorInvalidValue;
+  const int BN = (epi == GEMM_OUT_SWIGLU_FP8) ? 256 : 128;
+  if (m_block_expert && (N % BN)) return cudaErrorInvalidValue;
+  if (BN == 256 && (Nb % 256)) return cudaErrorInvalidValue;  // SF tiles of a 256-row B block must exist
+  CUtensorMap ta, tb;
+  if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, K, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, Nb, K, 128, BN, CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  GemmParams p{};
+  p.M = M; p.N = N; p.K = K;
+  p.sfa = sfa; p.sfb = sfb;
+  p.sfa_row_blocks = ceil_div(M, 128);
+  p.sfb_row_blocks = ceil_div(Nb, 128);
+  p.out = out; p.ldo = ldo; p.out_sf = out_sf; p.swiglu_limit = swiglu_limit;
+  p.m_block_expert = m_block_expert; p.num_m_blocks_dev = num_m_blocks_dev; p.status = status;
+  const int mblocks = m_block_expert ? max_m_blocks : ceil_div(M, 128);
+  const int max_tiles = mblocks * ceil_div(N, BN);
+  if (epi == GEMM_OUT_SWIGLU_FP8) return launch<KIND_MXF8, EPI_SWIGLU_FP8, 256, 4, 1>(ta, tb, p, max_tiles, num_sms, s);
+  if (epi == GEMM_OUT_F32) return launch<KIND_MXF8, EPI_F32, 128, 6, 2>(ta, tb, p, max_tiles, num_sms, s);
+  return launch<KIND_MXF8, EPI_BF16, 128, 6, 2>(ta, tb, p, max_tiles, num_sms, s);
+}
+
+cudaError_t gemm_bf16(const void* A, int lda, const void* B, int ldb, int M, int N, int K, int Nb, void* out, int ldo,
+                      int epi, const int* m_block_expert, const int* num_m_blocks_dev, int max_m_blocks, int* status,
+                      int num_sms, cudaStream_t s) {
+  if (M <= 0 || N <= 0) return cudaSuccess;
+  if (K % 64 || N % 16) return cudaErrorInvalidValue;
+  constexpr int BN = 128;
+  CUtensorMap ta, tb;
+  if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, M, uint64_t(lda) * 2, 64, 128,
+                    CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, Nb, uint64_t(ldb) * 2, 64, BN,
+                    CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  GemmParams p{};
+  p.M = M; p.N = N; p.K = K;
+  p.out = out; p.ldo = ldo;
+  p.m_block_expert = m_block_expert; p.num_m_blocks_dev = num_m_blocks_dev; p.status = status;
+  const int mblocks = m_block_expert ? max_m_blocks : ceil_div(M, 128);
+  const int max_tiles = mblocks * ceil_div(N, BN);
+  if (epi == GEMM_OUT_F32) return launch<KIND_BF16, EPI_F32, 128, 6, 2>(ta, tb, p, max_tiles, num_sms, s);
+  return launch<KIND_BF16, EPI_BF16, 128, 6, 2>(ta, tb, p, max_tiles, num_sms, s);
+}
+
+}  // namespace cb

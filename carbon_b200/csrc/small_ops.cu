@@ -1,0 +1,698 @@
+// CUDA-core kernels of the model: fp8 quantisers (UE8M0 1x128, SF-tile output), RMSNorm (+quant), RoPE,
+// router top-k, MoE row layout / gather-quant / weighted combine, mHC coefficient / mix kernels, embedding.
+//
+// Reference parity: router = king_v10/bundle_v9/cuda_moe_front.py:262-346 (score, bias-only ranking, lower-id ties,
+// renormalise, routed scale); quantisers = the pre-dispatch and q-norm quant of cuda_moe_prefill.py:3271-3452 and
+// cuda_prefill_fuse.py:81; mHC = cuda_sinkhorn.py:150-190 and cuda_mhc_packed.py:60-170 (math restated in
+// carbon_b200/ref/ops.py).  Every kernel here is written from that math; none reproduces another compiler's
+// instruction sequence.
+#include "common.cuh"
+#include "small_ops.h"
+
+namespace cb {
+
+// SF tile word index for row r (within the whole matrix) and k-block kb: returns the byte offset.
+CB_DEVICE size_t sf_byte_offset(int row, int kb, int row_blocks) {
+  const int rb = row >> 7, r = row & 127;
+  return ((size_t(kb >> 2) * row_blocks + rb) * 128 + (r & 31) * 4 + (r >> 5)) * 4 + (kb & 3);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// fp8 activation quantisation: one warp per (row, 512-column group); rows >= M (padding) get scale bytes 127.
+// x: bf16 [M, K] with row stride ldx; q: fp8 [M, K] row stride ldq; src_rows (optional): gather map.
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void act_quant_kernel(const __nv_bfloat16* __restrict__ x, int ldx, uint8_t* __restrict__ q, int ldq,
+                                 uint32_t* __restrict__ sf, int M, int K, int row_blocks,
+                                 const int* __restrict__ src_rows, int M_pad) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.y * 8 + warp;
+  const int kg = blockIdx.x;
+  if (row >= M_pad) return;
+  int src = row < M ? row : -1;
+  if (src >= 0 && src_rows) src = src_rows[row];
+  uint32_t word = 0;
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {                  // two halves of 256 columns = two k-blocks each
+    const int kb = kg * 4 + h * 2 + (lane >> 4); // lanes 0-15 -> even k-block, 16-31 -> odd
+    const int col = kb * 128 + (lane & 15) * 8;
+    float v[8];
+    bool in = src >= 0 && col < K;
+    if (in && col + 8 <= K) {
+      uint4 raw = *reinterpret_cast<const uint4*>(x + size_t(src) * ldx + col);
+      v[0] = bf16_lo(raw.x); v[1] = bf16_hi(raw.x); v[2] = bf16_lo(raw.y); v[3] = bf16_hi(raw.y);
+      v[4] = bf16_lo(raw.z); v[5] = bf16_hi(raw.z); v[6] = bf16_lo(raw.w); v[7] = bf16_hi(raw.w);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = (in && col + j < K) ? __bfloat162float(x[size_t(src) * ldx + col + j]) : 0.f;
+    }
+    float amax = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const uint32_t sb = ue8m0_for_amax(amax);
+    const float inv = ue8m0_inv(sb);
+    if (row < M && col < K) {
+      uint8_t* dst = q + size_t(row) * ldq + col;
+      if (col + 8 <= K) {
+        uint2 w;
+        w.x = pack_fp8x4(v[0] * inv, v[1] * inv, v[2] * inv, v[3] * inv);
+        w.y = pack_fp8x4(v[4] * inv, v[5] * inv, v[6] * inv, v[7] * inv);
+        *reinterpret_cast<uint2*>(dst) = w;
+      } else {
+        for (int j = 0; j < 8 && col + j < K; ++j) {
+          __nv_fp8_e4m3 f(v[j] * inv);
+          dst[j] = *reinterpret_cast<uint8_t*>(&f);
+        }
+      }
+    }
+    // byte (h*2 + lane/16) of the SF word
+    const uint32_t b = (kb * 128 < K) ? sb : 127u;
+    const uint32_t b_other = __shfl_sync(0xffffffffu, b, lane ^ 16);
+    if (lane == 0) word |= (b << (16 * h)) | (b_other << (16 * h + 8));
+  }
+  if (lane == 0) {
+    const int rb = row >> 7, r = row & 127;
+    sf[(size_t(kg) * row_blocks + rb) * 128 + (r & 31) * 4 + (r >> 5)] = word;
+  }
+}
+
+cudaError_t act_quant(const void* x, int ldx, void* q, int ldq, uint32_t* sf, int M, int K, const int* src_rows,
+                      cudaStream_t s) {
+  const int row_blocks = ceil_div(M, 128), M_pad = row_blocks * 128;
+  dim3 grid(ceil_div(K, 512), ceil_div(M_pad, 8));
+  act_quant_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx,
+                                        reinterpret_cast<uint8_t*>(q), ldq, sf, M, K, row_blocks, src_rows, M_pad);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// RMSNorm over rows: y = x * rsqrt(mean(x^2) + eps) * w. Optional bf16 out and/or fp8 + SF out.
+// One CTA (256 threads) per row; D % 8 == 0.
+// ---------------------------------------------------------------------------------------------------------------
+template <int MAXV>
+__global__ void rms_norm_kernel(const __nv_bfloat16* __restrict__ x, int ldx, const float* __restrict__ w,
+                                __nv_bfloat16* __restrict__ y, int ldy, uint8_t* __restrict__ q, uint32_t* sf,
+                                int row_blocks, int D, float eps) {
+  __shared__ float red[32];
+  const int row = blockIdx.x;
+  const __nv_bfloat16* xr = x + size_t(row) * ldx;
+  float v[MAXV * 8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int col = (i * blockDim.x + threadIdx.x) * 8;
+    if (col < D) {
+      uint4 raw = *reinterpret_cast<const uint4*>(xr + col);
+      v[i * 8 + 0] = bf16_lo(raw.x); v[i * 8 + 1] = bf16_hi(raw.x); v[i * 8 + 2] = bf16_lo(raw.y);
+      v[i * 8 + 3] = bf16_hi(raw.y); v[i * 8 + 4] = bf16_lo(raw.z); v[i * 8 + 5] = bf16_hi(raw.z);
+      v[i * 8 + 6] = bf16_lo(raw.w); v[i * 8 + 7] = bf16_hi(raw.w);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[i * 8 + j] * v[i * 8 + j];
+    }
+  }
+  ss = block_sum(ss, red);
+  const float r = rsqrtf(ss / D + eps);
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int col = (i * blockDim.x + threadIdx.x) * 8;
+    if (col < D) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[i * 8 + j] = __bfloat162float(__float2bfloat16_rn(v[i * 8 + j] * r * w[col + j]));
+      if (y) {
+        uint4 o;
+        o.x = pack_bf16x2(v[i * 8 + 0], v[i * 8 + 1]); o.y = pack_bf16x2(v[i * 8 + 2], v[i * 8 + 3]);
+        o.z = pack_bf16x2(v[i * 8 + 4], v[i * 8 + 5]); o.w = pack_bf16x2(v[i * 8 + 6], v[i * 8 + 7]);
+        *reinterpret_cast<uint4*>(y + size_t(row) * ldy + col) = o;
+      }
+    }
+  }
+  if (q) {
+    // 16 threads own one 128-column block (8 values each): reduce amax across them.
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      const int col = (i * blockDim.x + threadIdx.x) * 8;
+      float amax = 0.f;
+      if (col < D)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[i * 8 + j]));
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const uint32_t sb = ue8m0_for_amax(amax);
+      const float inv = ue8m0_inv(sb);
+      if (col < D) {
+        uint2 wq;
+        wq.x = pack_fp8x4(v[i * 8 + 0] * inv, v[i * 8 + 1] * inv, v[i * 8 + 2] * inv, v[i * 8 + 3] * inv);
+        wq.y = pack_fp8x4(v[i * 8 + 4] * inv, v[i * 8 + 5] * inv, v[i * 8 + 6] * inv, v[i * 8 + 7] * inv);
+        *reinterpret_cast<uint2*>(q + size_t(row) * D + col) = wq;
+        if ((threadIdx.x & 15) == 0)
+          reinterpret_cast<uint8_t*>(sf)[sf_byte_offset(row, col / 128, row_blocks)] = uint8_t(sb);
+      }
+    }
+  }
+}
+
+cudaError_t rms_norm(const void* x, int ldx, const float* w, void* y, int ldy, void* q, uint32_t* sf, int M, int D,
+                     float eps, cudaStream_t s) {
+  if (D % 8) return cudaErrorInvalidValue;
+  const int per = ceil_div(D, 256 * 8);
+  const int rb = ceil_div(M, 128);
+  auto xx = reinterpret_cast<const __nv_bfloat16*>(x);
+  auto yy = reinterpret_cast<__nv_bfloat16*>(y);
+  auto qq = reinterpret_cast<uint8_t*>(q);
+  if (q && D % 128) return cudaErrorInvalidValue;
+  if (per <= 1) rms_norm_kernel<1><<<M, 256, 0, s>>>(xx, ldx, w, yy, ldy, qq, sf, rb, D, eps);
+  else if (per <= 2) rms_norm_kernel<2><<<M, 256, 0, s>>>(xx, ldx, w, yy, ldy, qq, sf, rb, D, eps);
+  else if (per <= 4) rms_norm_kernel<4><<<M, 256, 0, s>>>(xx, ldx, w, yy, ldy, qq, sf, rb, D, eps);
+  else return cudaErrorInvalidValue;
+  return cudaGetLastError();
+}
+
+// SF padding rows (>= M inside the last 128-row block) get scale bytes 127 so every SF tile is defined.
+__global__ void sf_pad_kernel(uint32_t* sf, int M, int K, int row_blocks) {
+  const int kg = blockIdx.x;
+  const int r = (M & 127) + threadIdx.x;
+  if ((M & 127) == 0 || r >= 128) return;
+  const int row = (row_blocks - 1) * 128 + r;
+  sf[(size_t(kg) * row_blocks + (row >> 7)) * 128 + (r & 31) * 4 + (r >> 5)] = 0x7f7f7f7fu;
+}
+cudaError_t sf_pad(uint32_t* sf, int M, int K, cudaStream_t s) {
+  const int rb = ceil_div(M, 128);
+  if ((M & 127) == 0) return cudaSuccess;
+  sf_pad_kernel<<<ceil_div(K, 512), 128, 0, s>>>(sf, M, K, rb);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// RoPE (interleaved pairs) in place on bf16 x[T, H, *] at column offset `off`, width `dim`.
+// cos_sin: fp32 [max_pos, dim] laid out as (cos_0, sin_0, cos_1, sin_1, ...).
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void rope_kernel(__nv_bfloat16* x, int64_t stride_t, int64_t stride_h, int H, int off, int dim,
+                            const float* __restrict__ cos_sin, const int* __restrict__ pos, int inverse) {
+  const int t = blockIdx.x;
+  const int p = pos[t];
+  const int pairs = dim / 2;
+  for (int i = threadIdx.x; i < H * pairs; i += blockDim.x) {
+    const int h = i / pairs, j = i - h * pairs;
+    __nv_bfloat16* e = x + t * stride_t + h * stride_h + off + 2 * j;
+    const float c = cos_sin[size_t(p) * dim + 2 * j];
+    float sn = cos_sin[size_t(p) * dim + 2 * j + 1];
+    if (inverse) sn = -sn;
+    const float a = __bfloat162float(e[0]), b = __bfloat162float(e[1]);
+    e[0] = __float2bfloat16_rn(a * c - b * sn);
+    e[1] = __float2bfloat16_rn(a * sn + b * c);
+  }
+}
+cudaError_t rope_inplace(void* x, int T, int64_t stride_t, int64_t stride_h, int H, int off, int dim,
+                         const float* cos_sin, const int* pos, bool inverse, cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  rope_kernel<<<T, 128, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(x), stride_t, stride_h, H, off, dim, cos_sin, pos,
+                                inverse ? 1 : 0);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Router: one warp per token. act = f(logit); key = act + bias; top-k by key (ties -> lower id);
+// w = act[picked]; renormalise (optional); x route_scale.  E <= 1024, k <= 16.
+// score: 0 sigmoid, 1 sqrt(softplus), 2 softmax.
+// ---------------------------------------------------------------------------------------------------------------
+template <int EPL>  // experts per lane
+__global__ void router_kernel(const float* __restrict__ logits, const float* __restrict__ bias, int T, int E, int k,
+                              int score, int norm, float route_scale, float* __restrict__ w_out,
+                              int* __restrict__ id_out) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  const float* l = logits + size_t(warp) * E;
+  float act[EPL], key[EPL];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    const int e = i * 32 + lane;
+    act[i] = e < E ? l[e] : -INFINITY;
+    mx = fmaxf(mx, act[i]);
+  }
+  if (score == 2) {
+    mx = warp_max(mx);
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) { act[i] = (i * 32 + lane) < E ? __expf(act[i] - mx) : 0.f; s += act[i]; }
+    s = warp_sum(s);
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) act[i] /= s;
+  } else {
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      const float z = act[i];
+      if (score == 0) act[i] = 1.f / (1.f + expf(-z));
+      else act[i] = sqrtf(z > 20.f ? z : log1pf(expf(z)));   // softplus from its definition
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < EPL; ++i) {
+    const int e = i * 32 + lane;
+    key[i] = e < E ? act[i] + (bias ? bias[e] : 0.f) : -INFINITY;
+  }
+  float wsum = 0.f, my_w = 0.f;
+  int my_id = 0;
+  for (int r = 0; r < k; ++r) {
+    // local best (lowest id among equal keys: lower i first, strict >)
+    float bv = -INFINITY; int bi = 0x7fffffff; float ba = 0.f;
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      const int e = i * 32 + lane;
+      if (e < E && key[i] > bv) { bv = key[i]; bi = e; ba = act[i]; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      const float oa = __shfl_xor_sync(0xffffffffu, ba, o);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; ba = oa; }
+    }
+    if (lane == r) { my_w = ba; my_id = bi; }
+    wsum += ba;
+    if ((bi & 31) == lane) key[bi >> 5] = -INFINITY;
+  }
+  if (lane < k) {
+    float wv = my_w;
+    if (norm) wv = wv / (wsum + 1e-20f);
+    w_out[size_t(warp) * k + lane] = wv * route_scale;
+    id_out[size_t(warp) * k + lane] = my_id;
+  }
+}
+cudaError_t router_topk(const float* logits, const float* bias, int T, int E, int k, int score, bool norm,
+                        float route_scale, float* w, int* ids, cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  if (k > 32 || E > 1024) return cudaErrorInvalidValue;
+  const int blocks = ceil_div(T * 32, 256);
+#define CB_ROUTER(N) router_kernel<N><<<blocks, 256, 0, s>>>(logits, bias, T, E, k, score, norm ? 1 : 0, route_scale, w, ids)
+  if (E <= 64) CB_ROUTER(2);
+  else if (E <= 128) CB_ROUTER(4);
+  else if (E <= 256) CB_ROUTER(8);
+  else if (E <= 512) CB_ROUTER(16);
+  else CB_ROUTER(32);
+#undef CB_ROUTER
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// MoE layout: expert-sorted rows, every expert segment padded to 128 rows.
+//   ids [T*k] -> counts[E], seg_start[E], m_block_expert[max_blocks], num_blocks[1],
+//   slot_pos [T*k] (row of each (token, slot)), row_src [max_rows] (token of each row, -1 = padding).
+// One CTA of 1024 threads; E <= 1024.
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void moe_layout_kernel(const int* __restrict__ ids, int Tk, int k, int E, int max_blocks,
+                                  int* __restrict__ slot_pos, int* __restrict__ row_src,
+                                  int* __restrict__ m_block_expert, int* __restrict__ num_blocks,
+                                  int* __restrict__ counts_out) {
+  __shared__ int cnt[1024];
+  __shared__ int start[1024];
+  __shared__ int fill[1024];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) { cnt[e] = 0; fill[e] = 0; }
+  __syncthreads();
+  for (int i = threadIdx.x; i < Tk; i += blockDim.x) {
+    const int e = ids[i];
+    if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int e = 0; e < E; ++e) { start[e] = acc; acc += (cnt[e] + 127) & ~127; }
+    const int nb = acc >> 7;
+    num_blocks[0] = nb;
+    for (int e = 0, b = 0; e < E; ++e) {
+      const int nbe = (cnt[e] + 127) >> 7;
+      for (int j = 0; j < nbe && b < max_blocks; ++j) m_block_expert[b++] = e;
+    }
+    for (int b = nb; b < max_blocks; ++b) m_block_expert[b] = -1;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) if (counts_out) counts_out[e] = cnt[e];
+  const int max_rows = max_blocks * 128;
+  for (int r = threadIdx.x; r < max_rows; r += blockDim.x) row_src[r] = -1;
+  __syncthreads();
+  for (int i = threadIdx.x; i < Tk; i += blockDim.x) {
+    const int e = ids[i];
+    int pos = -1;
+    if (e >= 0 && e < E) {
+      pos = start[e] + atomicAdd(&fill[e], 1);
+      if (pos < max_rows) row_src[pos] = i / k;
+    }
+    slot_pos[i] = pos;
+  }
+}
+cudaError_t moe_layout(const int* ids, int T, int k, int E, int max_blocks, int* slot_pos, int* row_src,
+                       int* m_block_expert, int* num_blocks, int* counts, cudaStream_t s) {
+  if (E > 1024) return cudaErrorInvalidValue;
+  moe_layout_kernel<<<1, 1024, 0, s>>>(ids, T * k, k, E, max_blocks, slot_pos, row_src, m_block_expert, num_blocks,
+                                       counts);
+  return cudaGetLastError();
+}
+
+// Weighted combine: out[t] = sum_j w[t,j] * Y[slot_pos[t,j]] (+ add[t]); bf16 in/out, fp32 math. D % 8 == 0.
+__global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ Y, int ldy, const float* __restrict__ w,
+                                   const int* __restrict__ slot_pos, int k, const __nv_bfloat16* __restrict__ add,
+                                   __nv_bfloat16* __restrict__ out, int D) {
+  const int t = blockIdx.x;
+  for (int c = threadIdx.x * 8; c < D; c += blockDim.x * 8) {
+    float acc[8];
+    if (add) {
+      uint4 raw = *reinterpret_cast<const uint4*>(add + size_t(t) * D + c);
+      acc[0] = bf16_lo(raw.x); acc[1] = bf16_hi(raw.x); acc[2] = bf16_lo(raw.y); acc[3] = bf16_hi(raw.y);
+      acc[4] = bf16_lo(raw.z); acc[5] = bf16_hi(raw.z); acc[6] = bf16_lo(raw.w); acc[7] = bf16_hi(raw.w);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+    }
+    for (int j = 0; j < k; ++j) {
+      const int pos = slot_pos[t * k + j];
+      if (pos < 0) continue;
+      const float wv = w[t * k + j];
+      uint4 raw = *reinterpret_cast<const uint4*>(Y + size_t(pos) * ldy + c);
+      acc[0] += wv * bf16_lo(raw.x); acc[1] += wv * bf16_hi(raw.x); acc[2] += wv * bf16_lo(raw.y);
+      acc[3] += wv * bf16_hi(raw.y); acc[4] += wv * bf16_lo(raw.z); acc[5] += wv * bf16_hi(raw.z);
+      acc[6] += wv * bf16_lo(raw.w); acc[7] += wv * bf16_hi(raw.w);
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]); o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]); o.w = pack_bf16x2(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(out + size_t(t) * D + c) = o;
+  }
+}
+cudaError_t moe_combine(const void* Y, int ldy, const float* w, const int* slot_pos, int T, int k, const void* add,
+                        void* out, int D, cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  if (D % 8) return cudaErrorInvalidValue;
+  moe_combine_kernel<<<T, 128, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(Y), ldy, w, slot_pos, k,
+                                       reinterpret_cast<const __nv_bfloat16*>(add),
+                                       reinterpret_cast<__nv_bfloat16*>(out), D);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// mHC
+// ---------------------------------------------------------------------------------------------------------------
+// Coefficients from the stats projection. mix: fp32 [T, ld_mix] holding m_hi (cols 0..nmix-1) and m_lo
+// (cols nmix..2*nmix-1) of x_flat·fn^T (fn split into bf16 hi + lo parts); sumsq [T] = Σ x_flat².
+// One thread per token (hc == 4).
+__global__ void mhc_coeffs_kernel(const float* __restrict__ mix, int ld_mix, const float* __restrict__ sumsq,
+                                  const float* __restrict__ base, const float* __restrict__ scale, int T, int flat_dim,
+                                  int iters, float hc_eps, float rms_eps, float* __restrict__ pre,
+                                  float* __restrict__ post, float* __restrict__ comb) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  constexpr int HC = 4, NMIX = 24;
+  const float rsq = rsqrtf(sumsq[t] / flat_dim + rms_eps);
+  const float* m = mix + size_t(t) * ld_mix;
+  float mm[NMIX];
+#pragma unroll
+  for (int j = 0; j < NMIX; ++j) mm[j] = (m[j] + m[NMIX + j]) * rsq;
+#pragma unroll
+  for (int j = 0; j < HC; ++j) {
+    pre[t * HC + j] = 1.f / (1.f + expf(-(mm[j] * scale[0] + base[j]))) + hc_eps;
+    post[t * HC + j] = 2.f / (1.f + expf(-(mm[HC + j] * scale[1] + base[HC + j])));
+  }
+  float c[HC][HC];
+#pragma unroll
+  for (int i = 0; i < HC; ++i) {
+    float mx = -INFINITY;
+#pragma unroll
+    for (int o = 0; o < HC; ++o) { c[i][o] = mm[2 * HC + i * HC + o] * scale[2] + base[2 * HC + i * HC + o]; mx = fmaxf(mx, c[i][o]); }
+    float s = 0.f;
+#pragma unroll
+    for (int o = 0; o < HC; ++o) { c[i][o] = expf(c[i][o] - mx); s += c[i][o]; }
+#pragma unroll
+    for (int o = 0; o < HC; ++o) c[i][o] = c[i][o] / s + hc_eps;
+  }
+  // column normalise, then iters-1 (row, column) passes
+#pragma unroll
+  for (int o = 0; o < HC; ++o) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < HC; ++i) s += c[i][o];
+#pragma unroll
+    for (int i = 0; i < HC; ++i) c[i][o] /= (s + hc_eps);
+  }
+  for (int it = 1; it < iters; ++it) {
+#pragma unroll
+    for (int i = 0; i < HC; ++i) {
+      float s = 0.f;
+#pragma unroll
+      for (int o = 0; o < HC; ++o) s += c[i][o];
+#pragma unroll
+      for (int o = 0; o < HC; ++o) c[i][o] /= (s + hc_eps);
+    }
+#pragma unroll
+    for (int o = 0; o < HC; ++o) {
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < HC; ++i) s += c[i][o];
+#pragma unroll
+      for (int i = 0; i < HC; ++i) c[i][o] /= (s + hc_eps);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < HC; ++i)
+#pragma unroll
+    for (int o = 0; o < HC; ++o) comb[t * 16 + i * HC + o] = c[i][o];
+}
+cudaError_t mhc_coeffs(const float* mix, int ld_mix, const float* sumsq, const float* base, const float* scale, int T,
+                       int flat_dim, int iters, float hc_eps, float rms_eps, float* pre, float* post, float* comb,
+                       cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  mhc_coeffs_kernel<<<ceil_div(T, 128), 128, 0, s>>>(mix, ld_mix, sumsq, base, scale, T, flat_dim, iters, hc_eps,
+                                                     rms_eps, pre, post, comb);
+  return cudaGetLastError();
+}
+
+// Head coefficients: pre_j = sigmoid(m_j*rsq*scale + base_j) + eps from a [T, 2*HC] hi/lo projection.
+__global__ void mhc_head_coeffs_kernel(const float* __restrict__ mix, int ld_mix, const float* __restrict__ sumsq,
+                                       const float* __restrict__ base, const float* __restrict__ scale, int T,
+                                       int flat_dim, float hc_eps, float rms_eps, float* __restrict__ pre) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  const float rsq = rsqrtf(sumsq[t] / flat_dim + rms_eps);
+  const float* m = mix + size_t(t) * ld_mix;
+  for (int j = 0; j < 4; ++j)
+    pre[t * 4 + j] = 1.f / (1.f + expf(-((m[j] + m[4 + j]) * rsq * scale[0] + base[j]))) + hc_eps;
+}
+cudaError_t mhc_head_coeffs(const float* mix, int ld_mix, const float* sumsq, const float* base, const float* scale,
+                            int T, int flat_dim, float hc_eps, float rms_eps, float* pre, cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  mhc_head_coeffs_kernel<<<ceil_div(T, 128), 128, 0, s>>>(mix, ld_mix, sumsq, base, scale, T, flat_dim, hc_eps,
+                                                          rms_eps, pre);
+  return cudaGetLastError();
+}
+
+// Pre-mix + RMSNorm (+ fp8 quant): y = RMSNorm(Σ_i pre_i X_i) * w.  X bf16 [T, 4, D]; one CTA per token.
+// Writes bf16 y (optional) and fp8 q + SF tiles (optional). The mixed sum is rounded to bf16 before the norm.
+template <int MAXV>
+__global__ void mhc_pre_norm_kernel(const __nv_bfloat16* __restrict__ X, const float* __restrict__ pre,
+                                    const float* __restrict__ w, int D, float eps, __nv_bfloat16* __restrict__ y,
+                                    uint8_t* __restrict__ q, uint32_t* __restrict__ sf, int row_blocks,
+                                    const int* __restrict__ rows) {
+  __shared__ float red[32];
+  const int t_out = blockIdx.x;
+  const int t = rows ? rows[t_out] : t_out;
+  const __nv_bfloat16* xr = X + size_t(t) * 4 * D;
+  const float p0 = pre[t * 4 + 0], p1 = pre[t * 4 + 1], p2 = pre[t * 4 + 2], p3 = pre[t * 4 + 3];
+  float v[MAXV * 8];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int col = (i * blockDim.x + threadIdx.x) * 8;
+    if (col < D) {
+      float a[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) a[j] = 0.f;
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        const float ps = s == 0 ? p0 : s == 1 ? p1 : s == 2 ? p2 : p3;
+        uint4 raw = *reinterpret_cast<const uint4*>(xr + size_t(s) * D + col);
+        a[0] += ps * bf16_lo(raw.x); a[1] += ps * bf16_hi(raw.x); a[2] += ps * bf16_lo(raw.y);
+        a[3] += ps * bf16_hi(raw.y); a[4] += ps * bf16_lo(raw.z); a[5] += ps * bf16_hi(raw.z);
+        a[6] += ps * bf16_lo(raw.w); a[7] += ps * bf16_hi(raw.w);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[i * 8 + j] = __bfloat162float(__float2bfloat16_rn(a[j]));
+        ss += v[i * 8 + j] * v[i * 8 + j];
+      }
+    }
+  }
+  ss = block_sum(ss, red);
+  const float r = rsqrtf(ss / D + eps);
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int col = (i * blockDim.x + threadIdx.x) * 8;
+    float amax = 0.f;
+    if (col < D) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[i * 8 + j] = __bfloat162float(__float2bfloat16_rn(v[i * 8 + j] * r * w[col + j]));
+        amax = fmaxf(amax, fabsf(v[i * 8 + j]));
+      }
+      if (y) {
+        uint4 o;
+        o.x = pack_bf16x2(v[i * 8 + 0], v[i * 8 + 1]); o.y = pack_bf16x2(v[i * 8 + 2], v[i * 8 + 3]);
+        o.z = pack_bf16x2(v[i * 8 + 4], v[i * 8 + 5]); o.w = pack_bf16x2(v[i * 8 + 6], v[i * 8 + 7]);
+        *reinterpret_cast<uint4*>(y + size_t(t_out) * D + col) = o;
+      }
+    }
+    if (q) {
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const uint32_t sb = ue8m0_for_amax(amax);
+      const float inv = ue8m0_inv(sb);
+      if (col < D) {
+        uint2 wq;
+        wq.x = pack_fp8x4(v[i * 8 + 0] * inv, v[i * 8 + 1] * inv, v[i * 8 + 2] * inv, v[i * 8 + 3] * inv);
+        wq.y = pack_fp8x4(v[i * 8 + 4] * inv, v[i * 8 + 5] * inv, v[i * 8 + 6] * inv, v[i * 8 + 7] * inv);
+        *reinterpret_cast<uint2*>(q + size_t(t_out) * D + col) = wq;
+        if ((threadIdx.x & 15) == 0)
+          reinterpret_cast<uint8_t*>(sf)[sf_byte_offset(t_out, col / 128, row_blocks)] = uint8_t(sb);
+      }
+    }
+  }
+}
+cudaError_t mhc_pre_norm(const void* X, const float* pre, const float* w, int T, int D, float eps, void* y, void* q,
+                         uint32_t* sf, const int* rows, cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  if (D % 128) return cudaErrorInvalidValue;
+  const int per = ceil_div(D, 256 * 8), rb = ceil_div(T, 128);
+  auto XX = reinterpret_cast<const __nv_bfloat16*>(X);
+  auto yy = reinterpret_cast<__nv_bfloat16*>(y);
+  auto qq = reinterpret_cast<uint8_t*>(q);
+  if (per <= 1) mhc_pre_norm_kernel<1><<<T, 256, 0, s>>>(XX, pre, w, D, eps, yy, qq, sf, rb, rows);
+  else if (per <= 2) mhc_pre_norm_kernel<2><<<T, 256, 0, s>>>(XX, pre, w, D, eps, yy, qq, sf, rb, rows);
+  else if (per <= 4) mhc_pre_norm_kernel<4><<<T, 256, 0, s>>>(XX, pre, w, D, eps, yy, qq, sf, rb, rows);
+  else return cudaErrorInvalidValue;
+  return cudaGetLastError();
+}
+
+// Post-mix: Xn[o] = bf16(post_o * out + Σ_i comb[i][o] X_i); also sumsq[t] = Σ Xn² (for the next stats).
+// X, Xn bf16 [T, 4, D] (may alias: every element is read before it is written by the same thread); out bf16 [T, D].
+__global__ void mhc_post_mix_kernel(const __nv_bfloat16* X, const __nv_bfloat16* __restrict__ out,
+                                    const float* __restrict__ post, const float* __restrict__ comb, int D,
+                                    __nv_bfloat16* Xn, float* __restrict__ sumsq) {
+  __shared__ float red[32];
+  const int t = blockIdx.x;
+  float pst[4], cb[16];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) pst[j] = post[t * 4 + j];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) cb[j] = comb[t * 16 + j];
+  const __nv_bfloat16* xr = X + size_t(t) * 4 * D;
+  __nv_bfloat16* xo = Xn + size_t(t) * 4 * D;
+  float ss = 0.f;
+  for (int col = threadIdx.x * 8; col < D; col += blockDim.x * 8) {
+    float xs[4][8], ov[8];
+    uint4 r0 = *reinterpret_cast<const uint4*>(out + size_t(t) * D + col);
+    ov[0] = bf16_lo(r0.x); ov[1] = bf16_hi(r0.x); ov[2] = bf16_lo(r0.y); ov[3] = bf16_hi(r0.y);
+    ov[4] = bf16_lo(r0.z); ov[5] = bf16_hi(r0.z); ov[6] = bf16_lo(r0.w); ov[7] = bf16_hi(r0.w);
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      uint4 raw = *reinterpret_cast<const uint4*>(xr + size_t(s) * D + col);
+      xs[s][0] = bf16_lo(raw.x); xs[s][1] = bf16_hi(raw.x); xs[s][2] = bf16_lo(raw.y); xs[s][3] = bf16_hi(raw.y);
+      xs[s][4] = bf16_lo(raw.z); xs[s][5] = bf16_hi(raw.z); xs[s][6] = bf16_lo(raw.w); xs[s][7] = bf16_hi(raw.w);
+    }
+#pragma unroll
+    for (int o = 0; o < 4; ++o) {
+      float r[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float a = pst[o] * ov[j];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) a += cb[i * 4 + o] * xs[i][j];
+        r[j] = __bfloat162float(__float2bfloat16_rn(a));
+        ss += r[j] * r[j];
+      }
+      uint4 w;
+      w.x = pack_bf16x2(r[0], r[1]); w.y = pack_bf16x2(r[2], r[3]);
+      w.z = pack_bf16x2(r[4], r[5]); w.w = pack_bf16x2(r[6], r[7]);
+      *reinterpret_cast<uint4*>(xo + size_t(o) * D + col) = w;
+    }
+  }
+  ss = block_sum(ss, red);
+  if (threadIdx.x == 0) sumsq[t] = ss;
+}
+cudaError_t mhc_post_mix(const void* X, const void* out, const float* post, const float* comb, int T, int D, void* Xn,
+                         float* sumsq, cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  if (D % 8) return cudaErrorInvalidValue;
+  mhc_post_mix_kernel<<<T, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(X),
+                                        reinterpret_cast<const __nv_bfloat16*>(out), post, comb, D,
+                                        reinterpret_cast<__nv_bfloat16*>(Xn), sumsq);
+  return cudaGetLastError();
+}
+
+// Embedding into hc streams: X[t, s, :] = E[ids[t]] for all s; sumsq[t] = hc * Σ E².  Rows of the table outside
+// [row_lo, row_lo + rows) are skipped (vocab-parallel shard) and written as zeros.
+__global__ void embed_hc_kernel(const __nv_bfloat16* __restrict__ table, int row_lo, int rows,
+                                const int* __restrict__ ids, int D, int hc, __nv_bfloat16* __restrict__ X,
+                                float* __restrict__ sumsq) {
+  __shared__ float red[32];
+  const int t = blockIdx.x;
+  const int id = ids[t] - row_lo;
+  const bool mine = id >= 0 && id < rows;
+  float ss = 0.f;
+  for (int col = threadIdx.x * 8; col < D; col += blockDim.x * 8) {
+    uint4 raw = mine ? *reinterpret_cast<const uint4*>(table + size_t(id) * D + col) : make_uint4(0, 0, 0, 0);
+    ss += bf16_lo(raw.x) * bf16_lo(raw.x) + bf16_hi(raw.x) * bf16_hi(raw.x) + bf16_lo(raw.y) * bf16_lo(raw.y) +
+          bf16_hi(raw.y) * bf16_hi(raw.y) + bf16_lo(raw.z) * bf16_lo(raw.z) + bf16_hi(raw.z) * bf16_hi(raw.z) +
+          bf16_lo(raw.w) * bf16_lo(raw.w) + bf16_hi(raw.w) * bf16_hi(raw.w);
+    for (int s = 0; s < hc; ++s) *reinterpret_cast<uint4*>(X + (size_t(t) * hc + s) * D + col) = raw;
+  }
+  if (sumsq) {
+    ss = block_sum(ss, red);
+    if (threadIdx.x == 0) sumsq[t] = ss * hc;
+  }
+}
+cudaError_t embed_hc(const void* table, int row_lo, int rows, const int* ids, int T, int D, int hc, void* X,
+                     float* sumsq, cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  embed_hc_kernel<<<T, 128, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(table), row_lo, rows, ids, D, hc,
+                                    reinterpret_cast<__nv_bfloat16*>(X), sumsq);
+  return cudaGetLastError();
+}
+
+// Row sum of squares of bf16 rows (length n): used where the producer of X did not emit it.
+__global__ void row_sumsq_kernel(const __nv_bfloat16* __restrict__ x, int64_t n, float* __restrict__ out) {
+  __shared__ float red[32];
+  const int t = blockIdx.x;
+  float ss = 0.f;
+  for (int64_t c = threadIdx.x * 8; c < n; c += blockDim.x * 8) {
+    uint4 raw = *reinterpret_cast<const uint4*>(x + size_t(t) * n + c);
+    ss += bf16_lo(raw.x) * bf16_lo(raw.x) + bf16_hi(raw.x) * bf16_hi(raw.x) + bf16_lo(raw.y) * bf16_lo(raw.y) +
+          bf16_hi(raw.y) * bf16_hi(raw.y) + bf16_lo(raw.z) * bf16_lo(raw.z) + bf16_hi(raw.z) * bf16_hi(raw.z) +
+          bf16_lo(raw.w) * bf16_lo(raw.w) + bf16_hi(raw.w) * bf16_hi(raw.w);
+  }
+  ss = block_sum(ss, red);
+  if (threadIdx.x == 0) out[t] = ss;
+}
+cudaError_t row_sumsq(const void* x, int T, int64_t n, float* out, cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  if (n % 8) return cudaErrorInvalidValue;
+  row_sumsq_kernel<<<T, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), n, out);
+  return cudaGetLastError();
+}
+
+// SwiGLU on a bf16 [T, 2I] tensor whose halves are (gate | up) -> bf16 [T, I].
+__global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int I, float limit,
+                                __nv_bfloat16* __restrict__ out) {
+  const int t = blockIdx.x;
+  for (int c = threadIdx.x; c < I; c += blockDim.x) {
+    float g = __bfloat162float(gu[size_t(t) * 2 * I + c]);
+    float u = __bfloat162float(gu[size_t(t) * 2 * I + I + c]);
+    if (limit > 0.f) { g = fminf(g, limit); u = fminf(fmaxf(u, -limit), limit); }
+    out[size_t(t) * I + c] = __float2bfloat16_rn(g / (1.f + expf(-g)) * u);
+  }
+}
+cudaError_t silu_mul(const void* gu, int T, int I, float limit, void* out, cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  silu_mul_kernel<<<T, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(gu), I, limit,
+                                    reinterpret_cast<__nv_bfloat16*>(out));
+  return cudaGetLastError();
+}
+
+}  // namespace cb

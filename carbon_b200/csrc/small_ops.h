@@ -1,0 +1,47 @@
+// Host launchers of the CUDA-core kernels (raw pointers + stream; no torch types, so they can be called from
+// plain C/C++ as well as from the Python bindings).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace cb {
+
+cudaError_t act_quant(const void* x, int ldx, void* q, int ldq, uint32_t* sf, int M, int K, const int* src_rows,
+                      cudaStream_t s);
+cudaError_t rms_norm(const void* x, int ldx, const float* w, void* y, int ldy, void* q, uint32_t* sf, int M, int D,
+                     float eps, cudaStream_t s);
+cudaError_t sf_pad(uint32_t* sf, int M, int K, cudaStream_t s);
+cudaError_t rope_inplace(void* x, int T, int64_t stride_t, int64_t stride_h, int H, int off, int dim,
+                         const float* cos_sin, const int* pos, bool inverse, cudaStream_t s);
+cudaError_t router_topk(const float* logits, const float* bias, int T, int E, int k, int score, bool norm,
+                        float route_scale, float* w, int* ids, cudaStream_t s);
+cudaError_t moe_layout(const int* ids, int T, int k, int E, int max_blocks, int* slot_pos, int* row_src,
+                       int* m_block_expert, int* num_blocks, int* counts, cudaStream_t s);
+cudaError_t moe_combine(const void* Y, int ldy, const float* w, const int* slot_pos, int T, int k, const void* add,
+                        void* out, int D, cudaStream_t s);
+cudaError_t mhc_coeffs(const float* mix, int ld_mix, const float* sumsq, const float* base, const float* scale, int T,
+                       int flat_dim, int iters, float hc_eps, float rms_eps, float* pre, float* post, float* comb,
+                       cudaStream_t s);
+cudaError_t mhc_head_coeffs(const float* mix, int ld_mix, const float* sumsq, const float* base, const float* scale,
+                            int T, int flat_dim, float hc_eps, float rms_eps, float* pre, cudaStream_t s);
+cudaError_t mhc_pre_norm(const void* X, const float* pre, const float* w, int T, int D, float eps, void* y, void* q,
+                         uint32_t* sf, const int* rows, cudaStream_t s);
+cudaError_t mhc_post_mix(const void* X, const void* out, const float* post, const float* comb, int T, int D, void* Xn,
+                         float* sumsq, cudaStream_t s);
+cudaError_t embed_hc(const void* table, int row_lo, int rows, const int* ids, int T, int D, int hc, void* X,
+                     float* sumsq, cudaStream_t s);
+cudaError_t row_sumsq(const void* x, int T, int64_t n, float* out, cudaStream_t s);
+cudaError_t silu_mul(const void* gu, int T, int I, float limit, void* out, cudaStream_t s);
+
+// tcgen05 GEMMs (gemm.cu)
+enum GemmEpiHost { GEMM_OUT_BF16 = 0, GEMM_OUT_SWIGLU_FP8 = 1, GEMM_OUT_F32 = 2 };
+// fp8 block-scaled: A [M,K] e4m3 + SF tiles, B [Nb,K] e4m3 + SF tiles. Dense when m_block_expert == nullptr.
+cudaError_t gemm_fp8(const void* A, const void* B, const uint32_t* sfa, const uint32_t* sfb, int M, int N, int K,
+                     int Nb, void* out, int ldo, int epi, uint32_t* out_sf, float swiglu_limit,
+                     const int* m_block_expert, const int* num_m_blocks_dev, int max_m_blocks, int* status,
+                     int num_sms, cudaStream_t s);
+cudaError_t gemm_bf16(const void* A, int lda, const void* B, int ldb, int M, int N, int K, int Nb, void* out, int ldo,
+                      int epi, const int* m_block_expert, const int* num_m_blocks_dev, int max_m_blocks, int* status,
+                      int num_sms, cudaStream_t s);
+
+}  // namespace cb

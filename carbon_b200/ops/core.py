@@ -1,0 +1,141 @@
+"""Wrappers of the CUDA-core kernels (``csrc/small_ops.cu``). CPU tensors run the fp32 oracle instead."""
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+from ..ref import ops as R
+from ._ext import ext
+from .quant import empty_sf, pack_sf
+
+SCORE_FUNCS = {"sigmoid": 0, "sqrtsoftplus": 1, "softmax": 2}
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, want_bf16: bool = True, want_fp8: bool = False):
+    """Returns y (bf16) and/or (q fp8, sf)."""
+    if not x.is_cuda:
+        y = R.rms_norm(x, w, eps)
+        outs = []
+        if want_bf16:
+            outs.append(y.to(x.dtype))
+        if want_fp8:
+            q, s = R.quant_fp8_rows(y)
+            outs.append((q, pack_sf(s)))
+        return outs[0] if len(outs) == 1 else tuple(outs)
+    M, D = x.shape
+    y = torch.empty(M, D, dtype=torch.bfloat16, device=x.device) if want_bf16 else None
+    q = torch.empty(M, D, dtype=torch.float8_e4m3fn, device=x.device) if want_fp8 else None
+    sf = empty_sf(M, D, x.device) if want_fp8 else None
+    ext().rms_norm(x, w, y, q, sf, float(eps))
+    if want_bf16 and want_fp8:
+        return y, (q, sf)
+    return y if want_bf16 else (q, sf)
+
+
+def rope_table(max_pos: int, dim: int, theta: float, device) -> torch.Tensor:
+    """fp32 [max_pos, dim] interleaved (cos_j, sin_j) pairs computed in fp64."""
+    cos, sin = R.rope_cos_sin(torch.arange(max_pos), dim, theta)
+    return torch.stack([cos, sin], dim=-1).reshape(max_pos, dim).contiguous().to(device)
+
+
+def rope_(x: torch.Tensor, off: int, dim: int, table: torch.Tensor, pos: torch.Tensor, inverse: bool = False):
+    """In-place RoPE on x[T, H, off:off+dim] (interleaved pairs)."""
+    if not x.is_cuda:
+        cs = table[pos.long()].view(x.shape[0], dim // 2, 2)
+        cos, sin = cs[..., 0][:, None, :], cs[..., 1][:, None, :]
+        if inverse:
+            sin = -sin
+        seg = x[..., off:off + dim].float()
+        a, b = seg[..., 0::2], seg[..., 1::2]
+        out = torch.empty_like(seg)
+        out[..., 0::2] = a * cos - b * sin
+        out[..., 1::2] = a * sin + b * cos
+        x[..., off:off + dim] = out.to(x.dtype)
+        return x
+    ext().rope(x, off, dim, table, pos, inverse)
+    return x
+
+
+def router_topk(logits: torch.Tensor, bias: Optional[torch.Tensor], k: int, score_func: str, route_scale: float,
+                norm: bool) -> Tuple[torch.Tensor, torch.Tensor]:
+    if not logits.is_cuda:
+        return R.router_topk(logits, bias, k, score_func, route_scale, norm)
+    T = logits.shape[0]
+    w = torch.empty(T, k, dtype=torch.float32, device=logits.device)
+    ids = torch.empty(T, k, dtype=torch.int32, device=logits.device)
+    ext().router_topk(logits.float().contiguous(), bias, k, SCORE_FUNCS[score_func], norm, float(route_scale), w, ids)
+    return w, ids
+
+
+class MoeLayout:
+    """Expert-sorted row layout of one MoE call (every expert segment padded to 128 rows)."""
+
+    def __init__(self, ids: torch.Tensor, n_experts: int, max_blocks: Optional[int] = None):
+        T, k = ids.shape
+        dev = ids.device
+        if max_blocks is None:
+            max_blocks = (T * k + 127) // 128 + n_experts
+        self.T, self.k, self.E, self.max_blocks = T, k, n_experts, max_blocks
+        self.slot_pos = torch.empty(T, k, dtype=torch.int32, device=dev)
+        self.row_src = torch.empty(max_blocks * 128, dtype=torch.int32, device=dev)
+        self.m_block_expert = torch.empty(max_blocks, dtype=torch.int32, device=dev)
+        self.num_blocks = torch.empty(1, dtype=torch.int32, device=dev)
+        self.counts = torch.empty(n_experts, dtype=torch.int32, device=dev)
+        if ids.is_cuda:
+            ext().moe_layout(ids.contiguous(), n_experts, self.slot_pos, self.row_src, self.m_block_expert,
+                             self.num_blocks, self.counts)
+        else:
+            self._cpu(ids)
+
+    def _cpu(self, ids):
+        T, k, E = self.T, self.k, self.E
+        flat = ids.reshape(-1).long()
+        counts = torch.bincount(flat, minlength=E)
+        start = torch.zeros(E, dtype=torch.long)
+        acc = 0
+        mbe = []
+        for e in range(E):
+            start[e] = acc
+            nb = (int(counts[e]) + 127) // 128
+            mbe += [e] * nb
+            acc += nb * 128
+        self.num_blocks[0] = len(mbe)
+        self.m_block_expert.fill_(-1)
+        self.m_block_expert[: len(mbe)] = torch.tensor(mbe, dtype=torch.int32)
+        self.row_src.fill_(-1)
+        fill = torch.zeros(E, dtype=torch.long)
+        for i in range(T * k):
+            e = int(flat[i])
+            pos = int(start[e] + fill[e])
+            fill[e] += 1
+            self.slot_pos.view(-1)[i] = pos
+            self.row_src[pos] = i // k
+        self.counts.copy_(counts.to(torch.int32))
+
+    @property
+    def rows(self) -> int:
+        return self.max_blocks * 128
+
+
+def moe_combine(Y: torch.Tensor, w: torch.Tensor, slot_pos: torch.Tensor, add: Optional[torch.Tensor],
+                T: int) -> torch.Tensor:
+    if not Y.is_cuda:
+        out = torch.zeros(T, Y.shape[1], dtype=torch.float32)
+        for j in range(slot_pos.shape[1]):
+            pos = slot_pos[:, j].long()
+            ok = pos >= 0
+            out[ok] += w[ok, j:j + 1].float() * Y[pos[ok]].float()
+        if add is not None:
+            out += add.float()
+        return out.to(Y.dtype)
+    out = torch.empty(T, Y.shape[1], dtype=torch.bfloat16, device=Y.device)
+    ext().moe_combine(Y, w, slot_pos, add, out)
+    return out
+
+
+def split_hi_lo(fn: torch.Tensor) -> torch.Tensor:
+    """fp32 [n, K] -> bf16 [2n, K] = [hi; lo] with hi = bf16(fn), lo = bf16(fn - hi): x·fn ≈ x·hi + x·lo."""
+    hi = fn.float().to(torch.bfloat16)
+    lo = (fn.float() - hi.float()).to(torch.bfloat16)
+    return torch.cat([hi, lo], dim=0).contiguous()

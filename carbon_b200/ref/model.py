@@ -1,0 +1,211 @@
+"""CPU fp32 oracle of the whole model (BASELINE config 1 and the source of truth for every GPU path).
+
+The model is a DeepSeek-V3/V4-style decoder:
+
+* **mHC residual**: the residual is ``hc`` parallel streams ``X [T, hc, D]``.  Each sublayer reads
+  ``y = Σ pre_i X_i`` (then RMSNorm) and writes ``X'_o = post_o·F(y) + Σ_i comb[i][o] X_i`` with (pre, post, comb)
+  computed from ``X`` itself (``ref.ops.mhc_coeffs``).  This is the computation behind the reference's mHC boundary
+  kernels (``king_v10/bundle_v9/cuda_mhc_packed.py:40-170``, ``cuda_sinkhorn.py:150-190``).
+* **MLA attention** (q_lora → q, kv_lora latent + shared RoPE key), optionally **DSA sparse**: a lightning indexer
+  scores keys and each query attends only to its top-k keys (``dec/cuda_paged_logits.py:35-37``,
+  ``exact_topk.py:14``).
+* **MoE**: biased top-k router + routed SwiGLU experts + shared expert (``moe_route.py:166-216``).
+
+This module is deliberately naive: full-sequence recompute, no cache, fp32 everywhere.
+"""
+from __future__ import annotations
+
+from collections import OrderedDict
+from typing import Dict, List, Tuple
+
+import torch
+
+from ..config import ModelConfig
+from . import ops
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# parameter declaration (this order is the random-init order; names are the checkpoint format)
+# ----------------------------------------------------------------------------------------------------------------------
+def param_shapes(cfg: ModelConfig) -> "OrderedDict[str, Tuple[Tuple[int, ...], str]]":
+    """name -> (shape, init) with init in {"normal", "ones", "zeros"}."""
+    D, H, hc = cfg.hidden_size, cfg.n_heads, cfg.hc_mult
+    p: "OrderedDict[str, Tuple[Tuple[int, ...], str]]" = OrderedDict()
+    p["embed.weight"] = ((cfg.vocab_size, D), "normal")
+    for i in range(cfg.n_layers):
+        L = f"layers.{i}."
+        for sub in ("attn_hc", "ffn_hc"):
+            p[L + sub + ".fn"] = ((cfg.hc_mix_dim, hc * D), "normal")
+            p[L + sub + ".base"] = ((cfg.hc_mix_dim,), "normal")
+            p[L + sub + ".scale"] = ((3,), "ones")
+        p[L + "attn_norm.weight"] = ((D,), "ones")
+        if cfg.q_lora_rank > 0:
+            p[L + "attn.wq_a.weight"] = ((cfg.q_lora_rank, D), "normal")
+            p[L + "attn.q_norm.weight"] = ((cfg.q_lora_rank,), "ones")
+            p[L + "attn.wq_b.weight"] = ((H * cfg.qk_head_dim, cfg.q_lora_rank), "normal")
+        else:
+            p[L + "attn.wq.weight"] = ((H * cfg.qk_head_dim, D), "normal")
+        p[L + "attn.wkv_a.weight"] = ((cfg.kv_lora_rank + cfg.qk_rope_head_dim, D), "normal")
+        p[L + "attn.kv_norm.weight"] = ((cfg.kv_lora_rank,), "ones")
+        p[L + "attn.wkv_b.weight"] = ((H * (cfg.qk_nope_head_dim + cfg.v_head_dim), cfg.kv_lora_rank), "normal")
+        p[L + "attn.wo.weight"] = ((D, H * cfg.v_head_dim), "normal")
+        if cfg.use_indexer:
+            qin = cfg.q_lora_rank if cfg.q_lora_rank > 0 else D
+            p[L + "attn.indexer.wq.weight"] = ((cfg.index_n_heads * cfg.index_head_dim, qin), "normal")
+            p[L + "attn.indexer.wk.weight"] = ((cfg.index_head_dim, D), "normal")
+            p[L + "attn.indexer.k_norm.weight"] = ((cfg.index_head_dim,), "ones")
+            p[L + "attn.indexer.k_norm.bias"] = ((cfg.index_head_dim,), "zeros")
+            p[L + "attn.indexer.weights_proj.weight"] = ((cfg.index_n_heads, D), "normal")
+        p[L + "ffn_norm.weight"] = ((D,), "ones")
+        if cfg.is_moe_layer(i):
+            E, I = cfg.n_routed_experts, cfg.moe_intermediate
+            p[L + "ffn.gate.weight"] = ((E, D), "normal")
+            p[L + "ffn.gate.bias"] = ((E,), "normal")
+            p[L + "ffn.experts.w1"] = ((E, I, D), "normal")
+            p[L + "ffn.experts.w3"] = ((E, I, D), "normal")
+            p[L + "ffn.experts.w2"] = ((E, D, I), "normal")
+            if cfg.n_shared_experts > 0:
+                Is = I * cfg.n_shared_experts
+                p[L + "ffn.shared.w1"] = ((Is, D), "normal")
+                p[L + "ffn.shared.w3"] = ((Is, D), "normal")
+                p[L + "ffn.shared.w2"] = ((D, Is), "normal")
+        else:
+            I = cfg.dense_intermediate
+            p[L + "ffn.w1"] = ((I, D), "normal")
+            p[L + "ffn.w3"] = ((I, D), "normal")
+            p[L + "ffn.w2"] = ((D, I), "normal")
+    p["head_hc.fn"] = ((hc, hc * D), "normal")
+    p["head_hc.base"] = ((hc,), "normal")
+    p["head_hc.scale"] = ((1,), "ones")
+    p["norm.weight"] = ((D,), "ones")
+    p["head.weight"] = ((cfg.vocab_size, D), "normal")
+    return p
+
+
+def init_weights(cfg: ModelConfig, seed: int = 0, device="cpu", dtype=torch.float32) -> Dict[str, torch.Tensor]:
+    """Seeded random init: every "normal" tensor ~ N(0, init_std²), drawn in declaration order from one generator."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    out: Dict[str, torch.Tensor] = {}
+    for name, (shape, kind) in param_shapes(cfg).items():
+        if kind == "normal":
+            t = torch.randn(shape, generator=g, device=device, dtype=torch.float32) * cfg.init_std
+        elif kind == "ones":
+            t = torch.ones(shape, device=device, dtype=torch.float32)
+        else:
+            t = torch.zeros(shape, device=device, dtype=torch.float32)
+        out[name] = t.to(dtype)
+    return out
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# forward
+# ----------------------------------------------------------------------------------------------------------------------
+class RefModel:
+    """Naive full-sequence fp32 model. ``forward(ids)`` for one sequence returns logits [S, V]."""
+
+    def __init__(self, cfg: ModelConfig, weights: Dict[str, torch.Tensor]):
+        self.cfg = cfg
+        self.w = {k: v.float() for k, v in weights.items()}
+
+    # -- sublayers -------------------------------------------------------------------------------------------------
+    def attention(self, i: int, h: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        cfg, w = self.cfg, self.w
+        L = f"layers.{i}.attn."
+        T, H = h.shape[0], cfg.n_heads
+        dn, dr, dv, r = cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.v_head_dim, cfg.kv_lora_rank
+        if cfg.q_lora_rank > 0:
+            q_lat = ops.rms_norm(h @ w[L + "wq_a.weight"].t(), w[L + "q_norm.weight"], cfg.rms_eps)
+            q = (q_lat @ w[L + "wq_b.weight"].t()).view(T, H, dn + dr)
+        else:
+            q_lat = h
+            q = (h @ w[L + "wq.weight"].t()).view(T, H, dn + dr)
+        q_nope, q_pe = q[..., :dn], ops.apply_rope(q[..., dn:], pos, cfg.rope_theta)
+        kv = h @ w[L + "wkv_a.weight"].t()
+        kv_c = ops.rms_norm(kv[:, :r], w[L + "kv_norm.weight"], cfg.rms_eps)
+        k_pe = ops.apply_rope(kv[:, None, r:], pos, cfg.rope_theta)            # [T,1,dr]
+        kvb = (kv_c @ w[L + "wkv_b.weight"].t()).view(T, H, dn + dv)
+        k = torch.cat([kvb[..., :dn], k_pe.expand(T, H, dr)], dim=-1)
+        v = kvb[..., dn:]
+        qf = torch.cat([q_nope, q_pe], dim=-1)
+        allowed = None
+        if cfg.use_indexer:
+            allowed = ops.topk_mask(self.indexer_logits(i, h, q_lat, pos), pos, pos, cfg.index_topk)
+        o = ops.causal_attention(qf, k, v, cfg.softmax_scale, pos, pos, allowed)
+        return o.reshape(T, H * dv) @ w[L + "wo.weight"].t()
+
+    def indexer_logits(self, i: int, h: torch.Tensor, q_lat: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        q, k, wt = self.indexer_qkw(i, h, q_lat, pos)
+        return ops.indexer_logits(q, k, wt)
+
+    def indexer_qkw(self, i, h, q_lat, pos):
+        cfg, w = self.cfg, self.w
+        L = f"layers.{i}.attn.indexer."
+        T, Hi, Di, dr = h.shape[0], cfg.index_n_heads, cfg.index_head_dim, cfg.qk_rope_head_dim
+        q = (q_lat @ w[L + "wq.weight"].t()).view(T, Hi, Di)
+        q = torch.cat([ops.apply_rope(q[..., :dr], pos, cfg.rope_theta), q[..., dr:]], dim=-1)
+        k = ops.layer_norm(h @ w[L + "wk.weight"].t(), w[L + "k_norm.weight"], w[L + "k_norm.bias"], 1e-6)
+        k = torch.cat([ops.apply_rope(k[:, None, :dr], pos, cfg.rope_theta)[:, 0], k[:, dr:]], dim=-1)
+        wt = (h @ w[L + "weights_proj.weight"].t()) * (Hi ** -0.5) * (Di ** -0.5)
+        return q, k, wt
+
+    def ffn(self, i: int, h: torch.Tensor) -> torch.Tensor:
+        cfg, w = self.cfg, self.w
+        L = f"layers.{i}.ffn."
+        if not cfg.is_moe_layer(i):
+            return ops.swiglu(h @ w[L + "w1"].t(), h @ w[L + "w3"].t(), cfg.swiglu_limit) @ w[L + "w2"].t()
+        logits = h @ w[L + "gate.weight"].t()
+        wts, ids = ops.router_topk(logits, w[L + "gate.bias"], cfg.n_activated_experts, cfg.score_func,
+                                   cfg.route_scale, cfg.norm_topk_prob)
+        out = torch.zeros_like(h)
+        for e in range(cfg.n_routed_experts):
+            rows, slot = torch.nonzero(ids == e, as_tuple=True)
+            if rows.numel() == 0:
+                continue
+            x = h[rows]
+            y = ops.swiglu(x @ w[L + "experts.w1"][e].t(), x @ w[L + "experts.w3"][e].t(), cfg.swiglu_limit)
+            y = y @ w[L + "experts.w2"][e].t()
+            out.index_add_(0, rows, y * wts[rows, slot][:, None])
+        if cfg.n_shared_experts > 0:
+            out = out + ops.swiglu(h @ w[L + "shared.w1"].t(), h @ w[L + "shared.w3"].t(),
+                                   cfg.swiglu_limit) @ w[L + "shared.w2"].t()
+        return out
+
+    def hc_sublayer(self, X, prefix: str, norm_w: torch.Tensor, fn_apply) -> torch.Tensor:
+        cfg, w = self.cfg, self.w
+        pre, post, comb = ops.mhc_coeffs(X, w[prefix + ".fn"], w[prefix + ".base"], w[prefix + ".scale"],
+                                         cfg.hc_mult, cfg.sinkhorn_iters, cfg.hc_eps, cfg.rms_eps)
+        y = ops.rms_norm(ops.mhc_pre_mix(X, pre), norm_w, cfg.rms_eps)
+        return ops.mhc_post_mix(X, fn_apply(y), post, comb)
+
+    # -- whole model -----------------------------------------------------------------------------------------------
+    def forward(self, ids: torch.Tensor, pos: torch.Tensor = None) -> torch.Tensor:
+        cfg, w = self.cfg, self.w
+        T = ids.shape[0]
+        pos = torch.arange(T) if pos is None else pos
+        X = w["embed.weight"][ids.long()][:, None, :].expand(T, cfg.hc_mult, cfg.hidden_size).clone()
+        for i in range(cfg.n_layers):
+            L = f"layers.{i}."
+            X = self.hc_sublayer(X, L + "attn_hc", w[L + "attn_norm.weight"], lambda y: self.attention(i, y, pos))
+            X = self.hc_sublayer(X, L + "ffn_hc", w[L + "ffn_norm.weight"], lambda y: self.ffn(i, y))
+        return self.head(X)
+
+    def head(self, X: torch.Tensor) -> torch.Tensor:
+        cfg, w = self.cfg, self.w
+        pre = ops.mhc_head_coeffs(X, w["head_hc.fn"], w["head_hc.base"], w["head_hc.scale"], cfg.hc_eps, cfg.rms_eps)
+        y = ops.rms_norm(ops.mhc_pre_mix(X, pre), w["norm.weight"], cfg.rms_eps)
+        return y @ w["head.weight"].t()
+
+    def greedy(self, prompt: torch.Tensor, n_new: int) -> Tuple[List[int], List[torch.Tensor]]:
+        """Recompute-everything greedy decode. Returns (new token ids, last-position logits of every step)."""
+        ids = prompt.clone()
+        toks, logits = [], []
+        for _ in range(n_new + 1):
+            lg = self.forward(ids)[-1]
+            logits.append(lg)
+            if len(toks) == n_new:
+                break
+            nxt = int(torch.argmax(lg))
+            toks.append(nxt)
+            ids = torch.cat([ids, torch.tensor([nxt], dtype=ids.dtype)])
+        return toks, logits

@@ -1,0 +1,245 @@
+"""Plain fp32 PyTorch restatements of every op. These are the numerics oracle for the CUDA kernels.
+
+Each function states the math the corresponding kernel must reproduce.  The reference has no unit oracle (its checks
+compare a new kernel with the sealed engine's bytes, ``king_v10/bundle_v9/moe_front.py:200-295``); here the oracle
+is this file, written from the definitions:
+
+* mHC stats / Sinkhorn / boundary: reconstructed from ``king_v10/bundle_v9/cuda_sinkhorn.py:150-190`` and
+  ``cuda_mhc_packed.py:60-170`` (pre = σ(·)+eps, post = 2σ(·), comb = Sinkhorn of a 4×4 logit block).
+* Router: sigmoid / sqrt-softplus / softmax score, bias only in the ranking key, ties to the lower expert id,
+  renormalise, × routed scale (``cuda_moe_front.py:262-346`` for the sqrt-softplus form).
+* fp8 quantisers: e4m3 with power-of-two (UE8M0) block scales, 1×128 for activations and 128×128 for weights.
+* DSA lightning indexer: ``logit[t,s] = Σ_h w[t,h]·relu(q[t,h]·k[s])`` (``dec/cuda_paged_logits.py:35-37``).
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import torch
+import torch.nn.functional as F
+
+FP8_MAX = 448.0
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# norms / activations
+# ----------------------------------------------------------------------------------------------------------------------
+def rms_norm(x: torch.Tensor, w: Optional[torch.Tensor], eps: float) -> torch.Tensor:
+    xf = x.float()
+    y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return y * w.float() if w is not None else y
+
+
+def layer_norm(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float) -> torch.Tensor:
+    return F.layer_norm(x.float(), (x.shape[-1],), w.float(), b.float(), eps)
+
+
+def swiglu(g: torch.Tensor, u: torch.Tensor, limit: float = 0.0) -> torch.Tensor:
+    if limit > 0:
+        g = g.clamp(max=limit)
+        u = u.clamp(-limit, limit)
+    return F.silu(g) * u
+
+
+def softplus(x: torch.Tensor) -> torch.Tensor:
+    """log(1 + e^x) from its definition, with the large-x cutoff (x > 20 => x)."""
+    return torch.where(x > 20.0, x, torch.log1p(torch.exp(torch.clamp(x, max=20.0))))
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# RoPE (interleaved pairs: (x[2i], x[2i+1]) rotated by pos·θ^(-2i/d))
+# ----------------------------------------------------------------------------------------------------------------------
+def rope_cos_sin(positions: torch.Tensor, dim: int, theta: float) -> Tuple[torch.Tensor, torch.Tensor]:
+    inv = 1.0 / (theta ** (torch.arange(0, dim, 2, dtype=torch.float64) / dim))
+    ang = positions.to(torch.float64)[:, None] * inv[None, :]
+    return torch.cos(ang).float(), torch.sin(ang).float()
+
+
+def apply_rope(x: torch.Tensor, positions: torch.Tensor, theta: float, inverse: bool = False) -> torch.Tensor:
+    """x: [T, ..., d] (d even); positions: [T]."""
+    d = x.shape[-1]
+    cos, sin = rope_cos_sin(positions, d, theta)
+    if inverse:
+        sin = -sin
+    shape = [x.shape[0]] + [1] * (x.dim() - 2) + [d // 2]
+    cos, sin = cos.view(shape), sin.view(shape)
+    xf = x.float()
+    x0, x1 = xf[..., 0::2], xf[..., 1::2]
+    out = torch.empty_like(xf)
+    out[..., 0::2] = x0 * cos - x1 * sin
+    out[..., 1::2] = x0 * sin + x1 * cos
+    return out
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# fp8 block quantisation with UE8M0 (power-of-two) scales
+# ----------------------------------------------------------------------------------------------------------------------
+def ue8m0_scale(amax: torch.Tensor) -> torch.Tensor:
+    """Smallest power of two s with amax / s <= 448 (s = 2^ceil(log2(amax/448))); amax == 0 gives s = 1."""
+    a = amax.float().clamp(min=1e-30)
+    e = torch.ceil(torch.log2(a / FP8_MAX))
+    s = torch.exp2(e)
+    return torch.where(amax > 0, s, torch.ones_like(s))
+
+
+def quant_fp8_rows(x: torch.Tensor, block: int = 128) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Per-row 1×block quantisation. Returns (q fp8 e4m3 [M,K], scale fp32 [M, ceil(K/block)])."""
+    M, K = x.shape
+    nb = (K + block - 1) // block
+    xp = F.pad(x.float(), (0, nb * block - K))
+    blocks = xp.view(M, nb, block)
+    s = ue8m0_scale(blocks.abs().amax(-1))
+    q = (blocks / s[..., None]).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
+    return q.view(M, nb * block)[:, :K].contiguous(), s
+
+
+def dequant_fp8_rows(q: torch.Tensor, s: torch.Tensor, block: int = 128) -> torch.Tensor:
+    M, K = q.shape
+    sf = s.repeat_interleave(block, dim=1)[:, :K]
+    return q.float() * sf
+
+
+def quant_fp8_blocks(w: torch.Tensor, block: int = 128) -> Tuple[torch.Tensor, torch.Tensor]:
+    """128×128 weight quantisation. Returns (q [N,K], scale fp32 [ceil(N/128), ceil(K/128)])."""
+    N, K = w.shape
+    nb, kb = (N + block - 1) // block, (K + block - 1) // block
+    wp = F.pad(w.float(), (0, kb * block - K, 0, nb * block - N))
+    blocks = wp.view(nb, block, kb, block)
+    s = ue8m0_scale(blocks.abs().amax(dim=(1, 3)))
+    q = (blocks / s[:, None, :, None]).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
+    return q.view(nb * block, kb * block)[:N, :K].contiguous(), s
+
+
+def dequant_fp8_blocks(q: torch.Tensor, s: torch.Tensor, block: int = 128) -> torch.Tensor:
+    N, K = q.shape
+    sf = s.repeat_interleave(block, 0).repeat_interleave(block, 1)[:N, :K]
+    return q.float() * sf
+
+
+def fp8_gemm(a_q, a_s, b_q, b_s) -> torch.Tensor:
+    """Block-scaled fp8 GEMM oracle: dequantise both operands and multiply in fp32. Returns [M, N] fp32."""
+    return dequant_fp8_rows(a_q, a_s) @ dequant_fp8_blocks(b_q, b_s).t()
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# mHC
+# ----------------------------------------------------------------------------------------------------------------------
+def sinkhorn(logits: torch.Tensor, iters: int, eps: float) -> torch.Tensor:
+    """logits [..., n, n] -> doubly-stochastic comb. Row softmax + eps, column normalise, then iters-1 more
+    (row, column) normalisation passes, each dividing by (sum + eps)."""
+    c = torch.softmax(logits.float(), dim=-1) + eps
+    c = c / (c.sum(-2, keepdim=True) + eps)
+    for _ in range(iters - 1):
+        c = c / (c.sum(-1, keepdim=True) + eps)
+        c = c / (c.sum(-2, keepdim=True) + eps)
+    return c
+
+
+def mhc_coeffs(X: torch.Tensor, fn: torch.Tensor, base: torch.Tensor, scale: torch.Tensor, hc: int,
+               iters: int, hc_eps: float, rms_eps: float):
+    """X [T, hc, D]; fn [hc*(2+hc), hc*D]; base [hc*(2+hc)]; scale [3].
+    Returns pre [T,hc], post [T,hc], comb [T,hc,hc]."""
+    T = X.shape[0]
+    xf = X.reshape(T, -1).float()
+    rsq = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + rms_eps)
+    m = (xf @ fn.float().t()) * rsq
+    pre = torch.sigmoid(m[:, :hc] * scale[0] + base[:hc]) + hc_eps
+    post = 2.0 * torch.sigmoid(m[:, hc:2 * hc] * scale[1] + base[hc:2 * hc])
+    comb = sinkhorn((m[:, 2 * hc:] * scale[2] + base[2 * hc:]).view(T, hc, hc), iters, hc_eps)
+    return pre, post, comb
+
+
+def mhc_head_coeffs(X, fn, base, scale, hc_eps, rms_eps):
+    T = X.shape[0]
+    xf = X.reshape(T, -1).float()
+    rsq = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + rms_eps)
+    m = (xf @ fn.float().t()) * rsq
+    return torch.sigmoid(m * scale[0] + base) + hc_eps
+
+
+def mhc_pre_mix(X: torch.Tensor, pre: torch.Tensor) -> torch.Tensor:
+    """y = Σ_i pre_i · X_i  -> [T, D]."""
+    return (X.float() * pre[:, :, None]).sum(1)
+
+
+def mhc_post_mix(X: torch.Tensor, out: torch.Tensor, post: torch.Tensor, comb: torch.Tensor) -> torch.Tensor:
+    """X'_o = post_o · out + Σ_i comb[i][o] · X_i  -> [T, hc, D]."""
+    return post[:, :, None] * out.float()[:, None, :] + torch.einsum("tio,tid->tod", comb, X.float())
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# router
+# ----------------------------------------------------------------------------------------------------------------------
+def router_topk(logits: torch.Tensor, bias: Optional[torch.Tensor], k: int, score_func: str, route_scale: float,
+                norm: bool, n_groups: int = 1, topk_groups: int = 1):
+    """logits [T, E] fp32. Returns (weights [T,k] fp32, ids [T,k] int32). Ties go to the lower expert id."""
+    lf = logits.float()
+    if score_func == "sigmoid":
+        act = torch.sigmoid(lf)
+    elif score_func == "sqrtsoftplus":
+        act = torch.sqrt(softplus(lf))
+    elif score_func == "softmax":
+        act = torch.softmax(lf, dim=-1)
+    else:
+        raise ValueError(score_func)
+    key = act + bias.float()[None, :] if bias is not None else act.clone()
+    T, E = key.shape
+    if n_groups > 1:
+        g = key.view(T, n_groups, E // n_groups)
+        gscore = g.topk(2, dim=-1).values.sum(-1)
+        keep = _stable_topk(gscore, topk_groups)
+        mask = torch.zeros(T, n_groups, dtype=torch.bool)
+        mask.scatter_(1, keep, True)
+        key = key.masked_fill(~mask.repeat_interleave(E // n_groups, dim=1), float("-inf"))
+    ids = _stable_topk(key, k)
+    w = act.gather(1, ids)
+    if norm:
+        w = w / (w.sum(-1, keepdim=True) + 1e-20)
+    return w * route_scale, ids.to(torch.int32)
+
+
+def _stable_topk(key: torch.Tensor, k: int) -> torch.Tensor:
+    """Top-k by value with ties broken toward the lower index (deterministic)."""
+    E = key.shape[-1]
+    # sort by (-value, index): stable sort on -value keeps index order for ties
+    order = torch.sort(-key, dim=-1, stable=True).indices
+    return order[..., :k]
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# attention
+# ----------------------------------------------------------------------------------------------------------------------
+def causal_attention(q, k, v, scale: float, q_pos: torch.Tensor, k_pos: torch.Tensor,
+                     allowed: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """q [Tq,H,dq], k [Tk,H,dq] or [Tk,1,dq], v [Tk,H,dv] or [Tk,1,dv].
+    Mask: k_pos <= q_pos, and (if given) allowed[Tq, Tk] bool. Returns [Tq, H, dv] fp32."""
+    qf, kf, vf = q.float(), k.float(), v.float()
+    if kf.shape[1] == 1:
+        kf = kf.expand(-1, qf.shape[1], -1)
+    if vf.shape[1] == 1:
+        vf = vf.expand(-1, qf.shape[1], -1)
+    s = torch.einsum("qhd,khd->hqk", qf, kf) * scale
+    mask = k_pos[None, :] <= q_pos[:, None]
+    if allowed is not None:
+        mask = mask & allowed
+    s = s.masked_fill(~mask[None], float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    return torch.einsum("hqk,khd->qhd", p, vf)
+
+
+def indexer_logits(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """q [Tq, Hi, d], k [Tk, d], w [Tq, Hi] -> logits [Tq, Tk] = Σ_h w[t,h]·relu(q[t,h]·k[s])."""
+    s = torch.einsum("qhd,kd->qhk", q.float(), k.float()).clamp(min=0)
+    return torch.einsum("qhk,qh->qk", s, w.float())
+
+
+def topk_mask(logits: torch.Tensor, q_pos: torch.Tensor, k_pos: torch.Tensor, topk: int) -> torch.Tensor:
+    """Boolean [Tq, Tk]: the top-k causal keys of each query (all causal keys when fewer than topk exist)."""
+    causal = k_pos[None, :] <= q_pos[:, None]
+    l = logits.masked_fill(~causal, float("-inf"))
+    k = min(topk, l.shape[1])
+    idx = _stable_topk(l, k)
+    m = torch.zeros_like(causal)
+    m.scatter_(1, idx, True)
+    return m & causal

@@ -1,0 +1,277 @@
+"""GPU numerics of every CUDA kernel against the plain-PyTorch fp32 oracle of the same op."""
+import pytest
+import torch
+
+from carbon_b200.ref import ops as R
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _ext():
+    from carbon_b200.ops._ext import ext
+
+    return ext()
+
+
+def rel_err(a, b):
+    a, b = a.float().cpu(), b.float().cpu()
+    return ((a - b).norm() / (b.norm() + 1e-12)).item()
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# quantisation
+# ----------------------------------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("M,K", [(1, 128), (37, 512), (200, 1536), (128, 7168), (5, 576 - 64)])
+def test_act_quant_matches_oracle(M, K):
+    from carbon_b200.ops.quant import quant_act, unpack_sf
+
+    torch.manual_seed(0)
+    x = (torch.randn(M, K) * 3).to(torch.bfloat16)
+    q, sf = quant_act(x.to(DEV))
+    q_ref, s_ref = R.quant_fp8_rows(x.float())
+    s = unpack_sf(sf.cpu(), M, K)
+    assert torch.equal(s, s_ref)
+    assert torch.equal(q.cpu().view(torch.uint8), q_ref.view(torch.uint8))
+
+
+def test_act_quant_gather_rows():
+    from carbon_b200.ops.quant import quant_act, unpack_sf
+
+    x = torch.randn(10, 256).to(torch.bfloat16)
+    src = torch.tensor([3, -1, 0, 9, 9, -1, 2], dtype=torch.int32)
+    q, sf = quant_act(x.to(DEV), src_rows=src.to(DEV))
+    xs = torch.where((src >= 0)[:, None], x.float()[src.clamp(min=0).long()], torch.zeros(()))
+    q_ref, s_ref = R.quant_fp8_rows(xs)
+    assert torch.equal(q.cpu().view(torch.uint8), q_ref.view(torch.uint8))
+    assert torch.equal(unpack_sf(sf.cpu(), 7, 256), s_ref)
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# GEMMs
+# ----------------------------------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("M,N,K", [(128, 128, 128), (256, 384, 512), (1, 256, 1024), (300, 576, 7168),
+                                   (1000, 1536, 2048), (77, 4096, 640)])
+def test_fp8_gemm_dense(M, N, K):
+    from carbon_b200.ops.gemm import fp8_gemm
+    from carbon_b200.ops.quant import Fp8Weight, quant_act
+
+    torch.manual_seed(1)
+    x = torch.randn(M, K).to(torch.bfloat16)
+    w = torch.randn(N, K) * 0.02
+    W = Fp8Weight.from_float(w)
+    Wd = Fp8Weight(W.q.to(DEV), W.sf.to(DEV), W.scale.to(DEV))
+    q, sf = quant_act(x.to(DEV))
+    out = fp8_gemm(q, sf, Wd, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    q_ref, s_ref = R.quant_fp8_rows(x.float())
+    ref = R.fp8_gemm(q_ref, s_ref, W.q, W.scale)
+    assert rel_err(out, ref) < 1e-5, rel_err(out, ref)
+    out_bf = fp8_gemm(q, sf, Wd)
+    assert rel_err(out_bf, ref) < 5e-3
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 128, 64), (200, 256, 512), (1, 128, 192), (513, 640, 1024)])
+def test_bf16_gemm(M, N, K):
+    from carbon_b200.ops.gemm import bf16_gemm
+
+    torch.manual_seed(2)
+    a = torch.randn(M, K).to(torch.bfloat16)
+    b = torch.randn(N, K).to(torch.bfloat16)
+    out = bf16_gemm(a.to(DEV), b.to(DEV), out_dtype=torch.float32)
+    ref = a.float() @ b.float().t()
+    assert rel_err(out, ref) < 1e-5
+
+
+def test_bf16_gemm_strided_a():
+    from carbon_b200.ops.gemm import bf16_gemm
+
+    a_full = torch.randn(64, 384).to(torch.bfloat16).to(DEV)
+    a = a_full[:, 128:320]                       # row stride 384 elements, 192 wide
+    b = torch.randn(256, 192).to(torch.bfloat16).to(DEV)
+    out = bf16_gemm(a, b, out_dtype=torch.float32)
+    assert rel_err(out, a.float() @ b.float().t()) < 1e-5
+
+
+def _grouped_case(T=300, E=8, k=2, D=512, N=256, seed=3):
+    from carbon_b200.ops.core import MoeLayout
+
+    g = torch.Generator().manual_seed(seed)
+    ids = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(torch.int32)
+    lay = MoeLayout(ids.to(DEV), E)
+    return ids, lay
+
+
+def test_moe_layout_and_grouped_fp8_gemm():
+    from carbon_b200.ops.gemm import fp8_gemm
+    from carbon_b200.ops.quant import Fp8Weight, quant_act
+
+    T, E, k, K, N = 300, 8, 2, 512, 256
+    ids, lay = _grouped_case(T, E, k, K, N)
+    torch.cuda.synchronize()
+    slot_pos = lay.slot_pos.cpu()
+    row_src = lay.row_src.cpu()
+    mbe = lay.m_block_expert.cpu()
+    nb = int(lay.num_blocks.cpu())
+    counts = torch.bincount(ids.view(-1).long(), minlength=E)
+    assert nb == int(((counts + 127) // 128).sum())
+    for t in range(T):
+        for j in range(k):
+            p = int(slot_pos[t, j])
+            assert row_src[p] == t and mbe[p // 128] == ids[t, j]
+    x = torch.randn(T, K).to(torch.bfloat16)
+    w = torch.randn(E, N, K) * 0.02
+    Ws = [Fp8Weight.from_float(w[e]) for e in range(E)]
+    Wq = torch.cat([W.q for W in Ws]).to(DEV)
+    from carbon_b200.ops.quant import pack_sf
+    Wsf = pack_sf(torch.cat([W.scale.repeat_interleave(128, 0)[:N] for W in Ws])).to(DEV)
+    Wall = Fp8Weight(Wq, Wsf, None)
+    q, sf = quant_act(x.to(DEV), src_rows=lay.row_src)
+    out = fp8_gemm(q, sf, Wall, out_dtype=torch.float32, m_block_expert=lay.m_block_expert,
+                   num_m_blocks=lay.num_blocks, n_per_group=N)
+    torch.cuda.synchronize()
+    out = out.cpu()
+    q_ref, s_ref = R.quant_fp8_rows(x.float())
+    xd = R.dequant_fp8_rows(q_ref, s_ref)
+    for t in range(0, T, 7):
+        for j in range(k):
+            e = int(ids[t, j])
+            ref = xd[t] @ Ws[e].dequant().t()
+            got = out[int(slot_pos[t, j])]
+            assert rel_err(got, ref) < 1e-5
+
+
+def test_grouped_swiglu_fp8_epilogue():
+    from carbon_b200.ops.gemm import fp8_gemm_swiglu, interleave_gate_up
+    from carbon_b200.ops.quant import Fp8Weight, pack_sf, quant_act, unpack_sf
+
+    T, E, k, K, I = 200, 4, 2, 256, 256
+    ids, lay = _grouped_case(T, E, k, K, 2 * I, seed=4)
+    x = torch.randn(T, K).to(torch.bfloat16)
+    w1 = torch.randn(E, I, K) * 0.05
+    w3 = torch.randn(E, I, K) * 0.05
+    Ws = [Fp8Weight.from_float(interleave_gate_up(w1[e], w3[e])) for e in range(E)]
+    Wall = Fp8Weight(torch.cat([W.q for W in Ws]).to(DEV),
+                     pack_sf(torch.cat([W.scale.repeat_interleave(128, 0)[:2 * I] for W in Ws])).to(DEV), None)
+    q, sf = quant_act(x.to(DEV), src_rows=lay.row_src)
+    act, act_sf = fp8_gemm_swiglu(q, sf, Wall, 0.0, lay.m_block_expert, lay.num_blocks, 2 * I)
+    torch.cuda.synchronize()
+    rows = lay.rows
+    a_s = unpack_sf(act_sf.cpu(), rows, I)
+    act_d = act.cpu().float() * a_s.repeat_interleave(128, 1)
+    q_ref, s_ref = R.quant_fp8_rows(x.float())
+    xd = R.dequant_fp8_rows(q_ref, s_ref)
+    slot_pos = lay.slot_pos.cpu()
+    for t in range(0, T, 5):
+        for j in range(k):
+            e = int(ids[t, j])
+            wd = Ws[e].dequant()
+            gu = xd[t] @ wd.t()
+            gu = gu.view(-1, 2, 128)
+            ref = R.swiglu(gu[:, 0].reshape(-1), gu[:, 1].reshape(-1))
+            got = act_d[int(slot_pos[t, j])]
+            assert rel_err(got, ref) < 0.04, rel_err(got, ref)
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# small ops
+# ----------------------------------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("M,D", [(3, 256), (65, 1536), (17, 7168)])
+def test_rms_norm(M, D):
+    from carbon_b200.ops.core import rms_norm
+    from carbon_b200.ops.quant import unpack_sf
+
+    x = torch.randn(M, D).to(torch.bfloat16)
+    w = torch.rand(D) + 0.5
+    y, (q, sf) = rms_norm(x.to(DEV), w.to(DEV), 1e-6, want_bf16=True, want_fp8=True)
+    ref = R.rms_norm(x.float(), w, 1e-6)
+    assert rel_err(y, ref) < 4e-3
+    deq = q.cpu().float() * unpack_sf(sf.cpu(), M, D).repeat_interleave(128, 1)
+    assert rel_err(deq, ref) < 0.04
+
+
+def test_rope_matches_oracle():
+    from carbon_b200.ops.core import rope_, rope_table
+
+    T, H, d, off = 9, 3, 64, 128
+    x = torch.randn(T, H, off + d).to(torch.bfloat16)
+    pos = torch.randint(0, 4000, (T,), dtype=torch.int32)
+    tab = rope_table(4096, d, 10000.0, DEV)
+    y = x.to(DEV)
+    rope_(y, off, d, tab, pos.to(DEV))
+    ref = R.apply_rope(x[..., off:].float(), pos, 10000.0)
+    assert rel_err(y[..., off:], ref) < 4e-3
+    assert torch.equal(y[..., :off].cpu(), x[..., :off])
+    rope_(y, off, d, tab, pos.to(DEV), inverse=True)
+    assert rel_err(y[..., off:], x[..., off:].float()) < 8e-3
+
+
+@pytest.mark.parametrize("score", ["sigmoid", "sqrtsoftplus", "softmax"])
+@pytest.mark.parametrize("E,k", [(8, 2), (256, 8), (384, 6)])
+def test_router_topk(score, E, k):
+    from carbon_b200.ops.core import router_topk
+
+    T = 97
+    logits = torch.randn(T, E)
+    bias = torch.randn(E) * 0.5
+    w, ids = router_topk(logits.to(DEV), bias.to(DEV), k, score, 2.5, True)
+    w_ref, ids_ref = R.router_topk(logits, bias, k, score, 2.5, True)
+    assert torch.equal(ids.cpu(), ids_ref)
+    assert rel_err(w, w_ref) < 1e-5
+
+
+def test_router_ties_prefer_lower_id():
+    from carbon_b200.ops.core import router_topk
+
+    logits = torch.zeros(4, 64)
+    w, ids = router_topk(logits.to(DEV), None, 6, "sigmoid", 1.0, True)
+    assert torch.equal(ids.cpu(), torch.arange(6, dtype=torch.int32).expand(4, 6))
+
+
+def test_moe_combine():
+    from carbon_b200.ops.core import moe_combine
+
+    T, k, D = 33, 3, 256
+    Y = torch.randn(200, D).to(torch.bfloat16)
+    pos = torch.randint(-1, 200, (T, k), dtype=torch.int32)
+    w = torch.rand(T, k)
+    add = torch.randn(T, D).to(torch.bfloat16)
+    out = moe_combine(Y.to(DEV), w.to(DEV), pos.to(DEV), add.to(DEV), T)
+    ref = moe_combine(Y, w, pos, add, T)
+    assert rel_err(out, ref) < 4e-3
+
+
+def test_mhc_kernels():
+    from carbon_b200.ops.core import split_hi_lo
+    from carbon_b200.ops.gemm import bf16_gemm
+
+    T, D, hc = 50, 256, 4
+    X = torch.randn(T, hc, D).to(torch.bfloat16)
+    fn = torch.randn(24, hc * D) * 0.02
+    base = torch.randn(24) * 0.1
+    scale = torch.tensor([1.0, 0.9, 1.1])
+    pre_r, post_r, comb_r = R.mhc_coeffs(X.float(), fn, base, scale, hc, 20, 1e-6, 1e-6)
+    Xd = X.to(DEV)
+    fhl = split_hi_lo(fn)
+    fpad = torch.zeros(64, hc * D, dtype=torch.bfloat16)
+    fpad[:48] = fhl
+    mix = bf16_gemm(Xd.view(T, -1), fpad.to(DEV), out_dtype=torch.float32)
+    ss = torch.empty(T, device=DEV)
+    _ext().row_sumsq(Xd.view(T, -1), ss)
+    pre = torch.empty(T, 4, device=DEV); post = torch.empty(T, 4, device=DEV); comb = torch.empty(T, 16, device=DEV)
+    _ext().mhc_coeffs(mix, ss, base.to(DEV), scale.to(DEV), hc * D, 20, 1e-6, 1e-6, pre, post, comb)
+    assert rel_err(pre, pre_r) < 1e-4 and rel_err(post, post_r) < 1e-4
+    assert rel_err(comb.view(T, 4, 4), comb_r) < 1e-4
+    w = torch.rand(D) + 0.5
+    y = torch.empty(T, D, dtype=torch.bfloat16, device=DEV)
+    _ext().mhc_pre_norm(Xd, pre_r.to(DEV), w.to(DEV), 1e-6, y, None, None, None)
+    y_ref = R.rms_norm(R.mhc_pre_mix(X.float(), pre_r), w, 1e-6)
+    assert rel_err(y, y_ref) < 5e-3
+    out = torch.randn(T, D).to(torch.bfloat16)
+    Xn = torch.empty_like(Xd)
+    ss2 = torch.empty(T, device=DEV)
+    _ext().mhc_post_mix(Xd, out.to(DEV), post_r.to(DEV), comb_r.reshape(T, 16).to(DEV), Xn, ss2)
+    Xn_ref = R.mhc_post_mix(X.float(), out.float(), post_r, comb_r)
+    assert rel_err(Xn, Xn_ref) < 5e-3
+    assert rel_err(ss2, Xn.float().pow(2).sum((1, 2))) < 1e-4
