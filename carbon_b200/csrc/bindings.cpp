@@ -212,7 +212,10 @@ void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor out, int64_t epi,
 
 }  // namespace
 
+void register_runtime(pybind11::module_& m);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  register_runtime(m);
   m.doc() = "carbon_b200 sm_100a kernels";
   m.def("act_quant", &act_quant);
   m.def("rms_norm", &rms_norm);

@@ -1,0 +1,236 @@
+"""Serving engine: requests, paged latent cache, prefill and decode steps, greedy sampling, CUDA-graph decode.
+
+Public API (what a user of the reference's engine calls — ``prepare_model`` / ``forward_model`` of the slot ABI,
+``king_v10/bundle_v9/slots.py:274-289``, wrap exactly this):
+
+    eng = Engine(model_cfg, device="cuda", source=WeightSource(cfg, seed=0))
+    out = eng.generate(prompts, max_new_tokens=16)          # greedy
+    logits = eng.prefill(reqs); logits = eng.decode(reqs)    # step level
+
+Decode steps are captured as CUDA graphs per batch bucket (the reference's decode / target-verify graph buckets,
+``dec/gemm_tables.py:51``); a step replays the graph of the smallest bucket ≥ batch after copying the step's
+metadata into the graph's static input buffers.
+"""
+from __future__ import annotations
+
+import math
+import time
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional, Sequence
+
+import torch
+
+from ..config import ModelConfig
+from ..models.deepseek import DeepseekModel, ForwardBatch
+from ..models.weights import WeightSource
+from .kv_cache import PagedLatentCache
+
+
+@dataclass
+class Request:
+    rid: int
+    prompt: List[int]
+    out: List[int] = field(default_factory=list)
+    pages: List[int] = field(default_factory=list)
+    n_cached: int = 0            # tokens whose KV is in the cache
+    done: bool = False
+
+    @property
+    def seq_len(self) -> int:
+        return len(self.prompt) + len(self.out)
+
+
+def _meta_ext():
+    from ..ops._ext import available, ext
+
+    return ext() if available() else None
+
+
+def decode_metadata(page_tables, seq_lens, page_size, pad_to, min_lmax=1):
+    e = _meta_ext()
+    if e is not None:
+        return e.decode_metadata(page_tables, seq_lens, page_size, pad_to, min_lmax)
+    B, Bp = len(seq_lens), max(len(seq_lens), pad_to)
+    Lmax = max([min_lmax, 1] + list(seq_lens))
+    out_loc = torch.zeros(Bp, dtype=torch.int32)
+    ks = torch.full((Bp, Lmax), -1, dtype=torch.int32)
+    nk = torch.ones(Bp, dtype=torch.int32)
+    pos = torch.zeros(Bp, dtype=torch.int32)
+    for b in range(B):
+        L = seq_lens[b]
+        for p in range(L):
+            ks[b, p] = page_tables[b][p // page_size] * page_size + p % page_size
+        out_loc[b] = ks[b, L - 1]
+        nk[b] = L
+        pos[b] = L - 1
+    for b in range(B, Bp):
+        ks[b, 0] = 0
+    return [out_loc, ks, nk, pos]
+
+
+def prefill_metadata(page_tables, starts, lens, page_size):
+    e = _meta_ext()
+    if e is not None:
+        return e.prefill_metadata(page_tables, starts, lens, page_size)
+    ol, ps = [], []
+    for b, (s, n) in enumerate(zip(starts, lens)):
+        for p in range(s, s + n):
+            ol.append(page_tables[b][p // page_size] * page_size + p % page_size)
+            ps.append(p)
+    return [torch.tensor(ol, dtype=torch.int32), torch.tensor(ps, dtype=torch.int32)]
+
+
+class Engine:
+    def __init__(self, cfg: ModelConfig, device="cpu", source: Optional[WeightSource] = None, num_pages: int = 256,
+                 page_size: int = 64, model: Optional[DeepseekModel] = None, cuda_graphs: bool = False,
+                 graph_buckets: Sequence[int] = (1, 2, 4, 8, 16, 32, 64, 128, 256), pctx=None, fp8: bool = True):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.model = model if model is not None else DeepseekModel(cfg, source or WeightSource(cfg), device,
+                                                                   fp8=fp8, pctx=pctx)
+        dtype = torch.bfloat16 if self.device.type == "cuda" else torch.float32
+        self.cache = PagedLatentCache(cfg, cfg.n_layers, num_pages, page_size, self.device, dtype)
+        # page 0 is a scratch page for padded rows of graph buckets
+        self._scratch = self.cache.alloc.alloc(1)
+        self.page_size = page_size
+        self._next_id = 0
+        self.cuda_graphs = cuda_graphs and self.device.type == "cuda"
+        self.graph_buckets = sorted(graph_buckets)
+        self._graphs: Dict[int, "_DecodeGraph"] = {}
+        self.stats = {"prefill_tokens": 0, "decode_tokens": 0}
+
+    # -- request lifecycle -------------------------------------------------------------------------------------------
+    def add_request(self, prompt: Sequence[int]) -> Request:
+        r = Request(self._next_id, list(int(t) for t in prompt))
+        self._next_id += 1
+        return r
+
+    def _ensure_pages(self, r: Request, n_tokens: int):
+        need = (n_tokens + self.page_size - 1) // self.page_size - len(r.pages)
+        if need > 0:
+            r.pages += list(self.cache.alloc.alloc(need))
+
+    def release(self, r: Request):
+        if r.pages:
+            self.cache.alloc.free(r.pages)
+            r.pages = []
+
+    # -- steps ---------------------------------------------------------------------------------------------------------
+    def prefill(self, reqs: List[Request]) -> torch.Tensor:
+        """Run every request's uncached prompt tokens; returns logits [B, V] of each request's last token."""
+        dev = self.device
+        ids, starts, lens = [], [], []
+        for r in reqs:
+            toks = (r.prompt + r.out)[r.n_cached:]
+            assert r.n_cached == 0, "prefill with a cached prefix is not supported by this step"
+            self._ensure_pages(r, r.seq_len)
+            ids += toks
+            starts.append(r.n_cached)
+            lens.append(len(toks))
+        out_loc, pos = prefill_metadata([r.pages for r in reqs], starts, lens, self.page_size)
+        cu = [0]
+        for n in lens:
+            cu.append(cu[-1] + n)
+        rows = torch.tensor([c - 1 for c in cu[1:]], dtype=torch.int32)
+        fb = ForwardBatch(ids=torch.tensor(ids, dtype=torch.int32).to(dev, non_blocking=True),
+                          pos=pos.to(dev, non_blocking=True), out_loc=out_loc.to(dev, non_blocking=True),
+                          is_prefill=True, cu_seqlens=cu, logits_rows=rows.to(dev, non_blocking=True))
+        logits = self.model.forward(fb, self.cache)
+        for r, n in zip(reqs, lens):
+            r.n_cached += n
+        self.stats["prefill_tokens"] += sum(lens)
+        return logits
+
+    def decode(self, reqs: List[Request], next_tokens: Sequence[int]) -> torch.Tensor:
+        """Append one token per request and run it; returns logits [B, V]."""
+        B = len(reqs)
+        for r, t in zip(reqs, next_tokens):
+            r.out.append(int(t))
+            self._ensure_pages(r, r.seq_len)
+        bucket = self._bucket(B) if self.cuda_graphs else B
+        out_loc, key_slots, n_keys, pos = decode_metadata([r.pages for r in reqs], [r.seq_len for r in reqs],
+                                                          self.page_size, bucket)
+        ids = torch.zeros(bucket, dtype=torch.int32)
+        ids[:B] = torch.tensor([r.out[-1] for r in reqs], dtype=torch.int32)
+        if self.cuda_graphs and bucket is not None:
+            g = self._graph(bucket, key_slots.shape[1])
+            logits = g.run(ids, pos, out_loc, key_slots, n_keys)[:B]
+        else:
+            dev = self.device
+            fb = ForwardBatch(ids=ids.to(dev), pos=pos.to(dev), out_loc=out_loc.to(dev), is_prefill=False,
+                              key_slots=key_slots.to(dev), n_keys=n_keys.to(dev))
+            logits = self.model.forward(fb, self.cache)[:B]
+        for r in reqs:
+            r.n_cached = r.seq_len
+        self.stats["decode_tokens"] += B
+        return logits
+
+    def _bucket(self, B: int) -> Optional[int]:
+        for b in self.graph_buckets:
+            if b >= B:
+                return b
+        return None
+
+    def _graph(self, bucket: int, lmax: int) -> "_DecodeGraph":
+        g = self._graphs.get(bucket)
+        if g is None or g.lmax < lmax:
+            # context grows: recapture with headroom (power-of-two rounding of the key width)
+            cap = max(lmax, 1 << math.ceil(math.log2(max(lmax, 2))))
+            g = _DecodeGraph(self, bucket, cap)
+            self._graphs[bucket] = g
+        return g
+
+    # -- convenience ---------------------------------------------------------------------------------------------------
+    def generate(self, prompts: List[Sequence[int]], max_new_tokens: int, return_logits: bool = False):
+        reqs = [self.add_request(p) for p in prompts]
+        logits = self.prefill(reqs)
+        history = [logits.float().cpu()] if return_logits else None
+        nxt = torch.argmax(logits.float(), dim=-1).tolist()
+        for _ in range(max_new_tokens - 1):
+            logits = self.decode(reqs, nxt)
+            if return_logits:
+                history.append(logits.float().cpu())
+            nxt = torch.argmax(logits.float(), dim=-1).tolist()
+        for r, t in zip(reqs, nxt):
+            r.out.append(int(t))
+        outs = [r.out for r in reqs]
+        for r in reqs:
+            self.release(r)
+        return (outs, history) if return_logits else outs
+
+
+class _DecodeGraph:
+    """One captured decode step for a fixed (bucket, key width). Inputs are static device buffers."""
+
+    def __init__(self, eng: Engine, bucket: int, lmax: int):
+        dev = eng.device
+        self.lmax = lmax
+        self.ids = torch.zeros(bucket, dtype=torch.int32, device=dev)
+        self.pos = torch.zeros(bucket, dtype=torch.int32, device=dev)
+        self.out_loc = torch.zeros(bucket, dtype=torch.int32, device=dev)
+        self.key_slots = torch.full((bucket, lmax), -1, dtype=torch.int32, device=dev)
+        self.key_slots[:, 0] = 0
+        self.n_keys = torch.ones(bucket, dtype=torch.int32, device=dev)
+        fb = ForwardBatch(ids=self.ids, pos=self.pos, out_loc=self.out_loc, is_prefill=False,
+                          key_slots=self.key_slots, n_keys=self.n_keys)
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(2):  # warm-up: lazy kernel attributes, allocator pools
+                eng.model.forward(fb, eng.cache)
+        torch.cuda.current_stream().wait_stream(s)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.logits = eng.model.forward(fb, eng.cache)
+
+    def run(self, ids, pos, out_loc, key_slots, n_keys) -> torch.Tensor:
+        self.ids.copy_(ids, non_blocking=True)
+        self.pos.copy_(pos, non_blocking=True)
+        self.out_loc.copy_(out_loc, non_blocking=True)
+        L = key_slots.shape[1]
+        self.key_slots[:, :L].copy_(key_slots, non_blocking=True)
+        if L < self.lmax:
+            self.key_slots[:, L:].fill_(-1)
+        self.n_keys.copy_(n_keys, non_blocking=True)
+        self.graph.replay()
+        return self.logits

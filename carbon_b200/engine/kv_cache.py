@@ -1,0 +1,49 @@
+"""Paged latent KV cache.
+
+Per layer the cache holds, for every token slot, the MLA latent row ``[kv_lora | rope]`` (the only per-token state
+absorbed MLA needs; one row serves all heads) and, when the model has a DSA indexer, the indexer key row.  Slots are
+grouped into pages of ``page_size`` tokens; a request owns a list of pages (its page table) and token ``p`` of the
+request lives in slot ``pages[p // page_size] * page_size + p % page_size``.
+
+Reference: the engine's ``token_to_kv_pool`` with fp8 SWA / fp4 compressed / fp4 index-K pools
+(``king_v10/bundle_v9/dec/index_reuse.py:10-17``, ``dec/cuda_decode_attn.py:41-43``).  Page allocation is done by
+the native block allocator in ``carbon_b200.engine.allocator`` (C++).
+"""
+from __future__ import annotations
+
+from typing import List
+
+import torch
+
+from ..config import ModelConfig
+from .allocator import BlockAllocator
+
+
+class PagedLatentCache:
+    def __init__(self, cfg: ModelConfig, n_layers: int, num_pages: int, page_size: int, device, dtype):
+        self.cfg = cfg
+        self.page_size = page_size
+        self.num_pages = num_pages
+        self.num_slots = num_pages * page_size
+        width = cfg.kv_lora_rank + cfg.qk_rope_head_dim
+        self.latent: List[torch.Tensor] = [torch.zeros(self.num_slots, width, dtype=dtype, device=device)
+                                           for _ in range(n_layers)]
+        self.index_k: List[torch.Tensor] = []
+        if cfg.use_indexer:
+            self.index_k = [torch.zeros(self.num_slots, cfg.index_head_dim, dtype=dtype, device=device)
+                            for _ in range(n_layers)]
+        self.alloc = BlockAllocator(num_pages)
+
+    def write_latent(self, layer: int, loc: torch.Tensor, rows: torch.Tensor) -> None:
+        self.latent[layer].index_copy_(0, loc.long(), rows.to(self.latent[layer].dtype))
+
+    def write_index_k(self, layer: int, loc: torch.Tensor, rows: torch.Tensor) -> None:
+        self.index_k[layer].index_copy_(0, loc.long(), rows.to(self.index_k[layer].dtype))
+
+    def bytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in self.latent + self.index_k)
+
+    @staticmethod
+    def bytes_per_token(cfg: ModelConfig, n_layers: int, elem: int = 2) -> int:
+        w = cfg.kv_lora_rank + cfg.qk_rope_head_dim + (cfg.index_head_dim if cfg.use_indexer else 0)
+        return w * elem * n_layers

@@ -1,0 +1,446 @@
+"""DeepSeek-V3/V4-style model graph (MLA + DSA indexer + MoE + mHC) for the serving engine.
+
+One implementation runs on two kinds of device tensors:
+
+* CPU fp32 — every op resolves to the oracle math in ``carbon_b200.ref``; used to test the engine logic (paged
+  latent cache, absorbed decode, batching) against the naive full-recompute oracle.
+* CUDA (B200) — bf16 activations, block-scaled fp8 weights (128×128 UE8M0) and the sm_100a kernels in
+  ``carbon_b200._C``.
+
+Layer structure (reference engine: ``sglang.srt.models.deepseek_v4`` patched by ``king_v10/bundle_v9/slots.py``):
+``X [T, hc, D]`` → mHC boundary (coeffs from X) → RMSNorm → MLA attention (+ indexer top-k) → post-mix →
+mHC boundary → RMSNorm → dense SwiGLU FFN or MoE (router top-k, routed experts, shared expert) → post-mix.
+Prefill uses the non-absorbed MLA form (k/v from wkv_b); decode uses the absorbed form over the latent cache.
+
+Parallelism: attention heads are split over TP ranks, experts over EP ranks (``carbon_b200.parallel``); with one
+rank every collective is the identity.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional
+
+import torch
+import torch.nn.functional as F
+
+from ..config import ModelConfig
+from ..ops import attention as A
+from ..ops import core as C
+from ..ops.gemm import bf16_gemm, fp8_gemm, fp8_gemm_swiglu, interleave_gate_up
+from ..ops.quant import Fp8Weight, quant_act, quantize_weight, stack_weights
+from ..ref import ops as R
+from .weights import WeightSource
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# linear layers
+# ----------------------------------------------------------------------------------------------------------------------
+class Lin:
+    """y = x·Wᵀ. CPU: fp32 weight. CUDA: block-scaled fp8 (default) or bf16."""
+
+    def __init__(self, w: torch.Tensor, device: torch.device, fp8: bool = True):
+        self.out_features, self.in_features = w.shape
+        if device.type == "cpu":
+            self.kind, self.w = "f32", w.float()
+        elif fp8 and self.in_features % 128 == 0:
+            self.kind, self.fw = "fp8", quantize_weight(w.to(device))
+        else:
+            # bf16 GEMM tiles need N % 16 == 0: pad the weight rows with zeros and slice the output
+            self.kind = "bf16"
+            n_pad = (-self.out_features) % 16
+            wp = torch.nn.functional.pad(w.float(), (0, 0, 0, n_pad)) if n_pad else w
+            self.w = wp.to(device=device, dtype=torch.bfloat16).contiguous()
+
+    def __call__(self, x: torch.Tensor, out_dtype=torch.bfloat16, xq=None) -> torch.Tensor:
+        if self.kind == "f32":
+            return x.float() @ self.w.t()
+        if self.kind == "fp8":
+            q, sf = xq if xq is not None else quant_act(x)
+            return fp8_gemm(q, sf, self.fw, out_dtype=out_dtype)
+        y = bf16_gemm(x, self.w, out_dtype=out_dtype)
+        return y if y.shape[1] == self.out_features else y[:, : self.out_features]
+
+
+class SwigluFFN:
+    """down(silu(gate(x)) * up(x)). CUDA: one fp8 GEMM with the SwiGLU+requant epilogue, then the down GEMM."""
+
+    def __init__(self, w1: torch.Tensor, w3: torch.Tensor, w2: torch.Tensor, device, limit: float):
+        self.limit = limit
+        if device.type == "cpu":
+            self.kind = "f32"
+            self.w1, self.w3, self.w2 = w1.float(), w3.float(), w2.float()
+        else:
+            self.kind = "fp8"
+            self.w13 = quantize_weight(interleave_gate_up(w1.to(device), w3.to(device)))
+            self.w2 = quantize_weight(w2.to(device))
+
+    def __call__(self, x: torch.Tensor, xq=None) -> torch.Tensor:
+        if self.kind == "f32":
+            return R.swiglu(x @ self.w1.t(), x @ self.w3.t(), self.limit) @ self.w2.t()
+        q, sf = xq if xq is not None else quant_act(x)
+        act, act_sf = fp8_gemm_swiglu(q, sf, self.w13, self.limit)
+        return fp8_gemm(act, act_sf, self.w2)
+
+
+@dataclass
+class HCParams:
+    fn: torch.Tensor        # CPU: fp32 [nmix, hc*D]; CUDA: bf16 [64, hc*D] = [hi; lo; 0-pad]
+    base: torch.Tensor
+    scale: torch.Tensor
+    nmix: int
+
+
+def make_hc(fn, base, scale, device) -> HCParams:
+    nmix = fn.shape[0]
+    if device.type == "cpu":
+        return HCParams(fn.float(), base.float(), scale.float(), nmix)
+    hl = C.split_hi_lo(fn.to(device))
+    rows = ((2 * nmix + 15) // 16) * 16
+    pad = torch.zeros(rows, fn.shape[1], dtype=torch.bfloat16, device=device)
+    pad[: 2 * nmix] = hl
+    return HCParams(pad, base.to(device).float(), scale.to(device).float(), nmix)
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# forward batch / cache
+# ----------------------------------------------------------------------------------------------------------------------
+@dataclass
+class ForwardBatch:
+    ids: torch.Tensor                      # [T] int32
+    pos: torch.Tensor                      # [T] int32 position of each token in its sequence
+    out_loc: torch.Tensor                  # [T] int32 cache slot each token's KV is written to
+    is_prefill: bool
+    cu_seqlens: Optional[List[int]] = None  # prefill: host boundaries of the sequences in `ids`
+    key_slots: Optional[torch.Tensor] = None  # decode: [B, Lmax] int32 slots of every key (incl. the new token)
+    n_keys: Optional[torch.Tensor] = None     # decode: [B] int32
+    logits_rows: Optional[torch.Tensor] = None  # rows that need logits (default: all)
+
+
+class Layer:
+    pass
+
+
+class DeepseekModel:
+    def __init__(self, cfg: ModelConfig, source: WeightSource, device="cpu", fp8: bool = True,
+                 pctx=None):
+        from ..parallel.context import ParallelCtx
+
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.on_gpu = self.device.type == "cuda"
+        self.pctx = pctx if pctx is not None else ParallelCtx.single()
+        self.fp8 = fp8
+        cfg.validate()
+        tp, ep = self.pctx.tp, self.pctx.ep
+        self.H_local = cfg.n_heads // tp
+        self.E_local = cfg.n_routed_experts // ep if cfg.n_routed_experts else 0
+        dev = self.device
+        get = lambda n, rows=None: source.get(n, dev, rows)
+        self.cos_sin = C.rope_table(cfg.max_position, cfg.qk_rope_head_dim, cfg.rope_theta, dev)
+        self.act_dtype = torch.bfloat16 if self.on_gpu else torch.float32
+        # vocab-parallel embedding/head: each rank keeps rows [v_lo, v_hi)
+        V = cfg.vocab_size
+        vs = (V + self.pctx.world - 1) // self.pctx.world if self.pctx.vocab_parallel else V
+        self.v_lo = self.pctx.rank * vs if self.pctx.vocab_parallel else 0
+        self.v_hi = min(V, self.v_lo + vs)
+        self.embed = get("embed.weight", slice(self.v_lo, self.v_hi)).to(self.act_dtype).contiguous()
+        self.head_w = Lin(get("head.weight", slice(self.v_lo, self.v_hi)), dev, fp8=False)
+        self.head_hc = make_hc(get("head_hc.fn"), get("head_hc.base"), get("head_hc.scale"), dev)
+        self.norm_w = get("norm.weight")
+        self.layers = [self._load_layer(i, get) for i in range(cfg.n_layers)]
+
+    # ------------------------------------------------------------------------------------------------------------------
+    def _load_layer(self, i: int, get) -> Layer:
+        cfg, dev, pc = self.cfg, self.device, self.pctx
+        L = Layer()
+        p = f"layers.{i}."
+        L.attn_hc = make_hc(get(p + "attn_hc.fn"), get(p + "attn_hc.base"), get(p + "attn_hc.scale"), dev)
+        L.ffn_hc = make_hc(get(p + "ffn_hc.fn"), get(p + "ffn_hc.base"), get(p + "ffn_hc.scale"), dev)
+        L.attn_norm = get(p + "attn_norm.weight")
+        L.ffn_norm = get(p + "ffn_norm.weight")
+        H, Hl, dn, dr, dv, r = cfg.n_heads, self.H_local, cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, \
+            cfg.v_head_dim, cfg.kv_lora_rank
+        h0, h1 = pc.tp_rank * Hl, (pc.tp_rank + 1) * Hl
+        a = p + "attn."
+        if cfg.q_lora_rank > 0:
+            L.wq_a = Lin(get(a + "wq_a.weight"), dev, self.fp8)
+            L.q_norm = get(a + "q_norm.weight")
+            L.wq_b = Lin(get(a + "wq_b.weight", slice(h0 * (dn + dr), h1 * (dn + dr))), dev, self.fp8)
+        else:
+            L.wq = Lin(get(a + "wq.weight", slice(h0 * (dn + dr), h1 * (dn + dr))), dev, self.fp8)
+        L.wkv_a = Lin(get(a + "wkv_a.weight"), dev, self.fp8)
+        L.kv_norm = get(a + "kv_norm.weight")
+        wkv_b = get(a + "wkv_b.weight", slice(h0 * (dn + dv), h1 * (dn + dv)))      # [Hl*(dn+dv), r]
+        L.wkv_b = Lin(wkv_b, dev, self.fp8)
+        wkv_b3 = wkv_b.view(Hl, dn + dv, r)
+        L.w_uk = wkv_b3[:, :dn, :].transpose(1, 2).contiguous().to(self.act_dtype)  # [Hl, r, dn]: q_abs = q_nope·w_ukᵀ
+        L.w_uv = wkv_b3[:, dn:, :].contiguous().to(self.act_dtype)                  # [Hl, dv, r]
+        wo = get(a + "wo.weight")                                                  # [D, H*dv]
+        L.wo = Lin(wo[:, h0 * dv:h1 * dv].contiguous(), dev, self.fp8)
+        if cfg.use_indexer:
+            ix = a + "indexer."
+            L.idx_wq = Lin(get(ix + "wq.weight"), dev, fp8=False)
+            L.idx_wk = Lin(get(ix + "wk.weight"), dev, fp8=False)
+            L.idx_kn_w, L.idx_kn_b = get(ix + "k_norm.weight"), get(ix + "k_norm.bias")
+            L.idx_wp = Lin(get(ix + "weights_proj.weight"), dev, fp8=False)
+        f = p + "ffn."
+        L.moe = cfg.is_moe_layer(i)
+        if not L.moe:
+            L.dense = SwigluFFN(get(f + "w1"), get(f + "w3"), get(f + "w2"), dev, cfg.swiglu_limit)
+        else:
+            E, El = cfg.n_routed_experts, self.E_local
+            e0 = pc.ep_rank * El
+            L.gate_w = get(f + "gate.weight").to(self.act_dtype).contiguous()
+            L.gate_b = get(f + "gate.bias")
+            if dev.type == "cpu":
+                L.e_w1 = get(f + "experts.w1", slice(e0, e0 + El))
+                L.e_w3 = get(f + "experts.w3", slice(e0, e0 + El))
+                L.e_w2 = get(f + "experts.w2", slice(e0, e0 + El))
+            else:
+                w13s, w2s = [], []
+                for e in range(e0, e0 + El):
+                    w1 = get(f + "experts.w1", slice(e, e + 1))[0]
+                    w3 = get(f + "experts.w3", slice(e, e + 1))[0]
+                    w13s.append(quantize_weight(interleave_gate_up(w1, w3)))
+                    w2s.append(quantize_weight(get(f + "experts.w2", slice(e, e + 1))[0]))
+                    del w1, w3
+                L.e_w13 = stack_weights(w13s)
+                L.e_w2 = stack_weights(w2s)
+                del w13s, w2s
+            L.shared = None
+            if cfg.n_shared_experts > 0:
+                L.shared = SwigluFFN(get(f + "shared.w1"), get(f + "shared.w3"), get(f + "shared.w2"), dev,
+                                     cfg.swiglu_limit)
+        return L
+
+    # ------------------------------------------------------------------------------------------------------------------
+    # mHC
+    # ------------------------------------------------------------------------------------------------------------------
+    def hc_coeffs(self, X: torch.Tensor, sumsq: Optional[torch.Tensor], hp: HCParams):
+        cfg = self.cfg
+        T = X.shape[0]
+        if not self.on_gpu:
+            return R.mhc_coeffs(X, hp.fn, hp.base, hp.scale, cfg.hc_mult, cfg.sinkhorn_iters, cfg.hc_eps, cfg.rms_eps)
+        from ..ops._ext import ext
+
+        mix = bf16_gemm(X.view(T, -1), hp.fn, out_dtype=torch.float32)
+        pre = torch.empty(T, 4, device=X.device)
+        post = torch.empty(T, 4, device=X.device)
+        comb = torch.empty(T, 4, 4, device=X.device)
+        ext().mhc_coeffs(mix, sumsq, hp.base, hp.scale, X.shape[1] * X.shape[2], cfg.sinkhorn_iters, cfg.hc_eps,
+                         cfg.rms_eps, pre, post, comb)
+        return pre, post, comb
+
+    def pre_norm(self, X, pre, w, want_fp8: bool):
+        """RMSNorm(Σ pre_i X_i)·w -> (bf16 h, (fp8 q, sf) or None)."""
+        if not self.on_gpu:
+            return R.rms_norm(R.mhc_pre_mix(X, pre), w, self.cfg.rms_eps), None
+        from ..ops._ext import ext
+        from ..ops.quant import empty_sf
+
+        T, _, D = X.shape
+        y = torch.empty(T, D, dtype=torch.bfloat16, device=X.device)
+        q = sf = None
+        if want_fp8:
+            q = torch.empty(T, D, dtype=torch.float8_e4m3fn, device=X.device)
+            sf = empty_sf(T, D, X.device)
+        ext().mhc_pre_norm(X, pre, w, self.cfg.rms_eps, y, q, sf, None)
+        return y, ((q, sf) if want_fp8 else None)
+
+    def post_mix(self, X, out, post, comb):
+        if not self.on_gpu:
+            return R.mhc_post_mix(X, out, post, comb), None
+        from ..ops._ext import ext
+
+        sumsq = torch.empty(X.shape[0], device=X.device)
+        ext().mhc_post_mix(X, out.contiguous(), post, comb.view(-1, 16), X, sumsq)   # in place
+        return X, sumsq
+
+    # ------------------------------------------------------------------------------------------------------------------
+    # attention
+    # ------------------------------------------------------------------------------------------------------------------
+    def attention(self, i: int, h: torch.Tensor, hq, fb: ForwardBatch, cache) -> torch.Tensor:
+        cfg, L = self.cfg, self.layers[i]
+        T, Hl = h.shape[0], self.H_local
+        dn, dr, dv, r = cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.v_head_dim, cfg.kv_lora_rank
+        if cfg.q_lora_rank > 0:
+            q_lat_raw = L.wq_a(h, xq=hq)
+            if self.on_gpu:
+                q_lat, q_lat_q = C.rms_norm(q_lat_raw, L.q_norm, cfg.rms_eps, want_bf16=True, want_fp8=True)
+            else:
+                q_lat, q_lat_q = R.rms_norm(q_lat_raw, L.q_norm, cfg.rms_eps), None
+            q = L.wq_b(q_lat, xq=q_lat_q).view(T, Hl, dn + dr)
+        else:
+            q_lat = h
+            q = L.wq(h, xq=hq).view(T, Hl, dn + dr)
+        if not self.on_gpu:
+            q = q.clone()
+        C.rope_(q, dn, dr, self.cos_sin, fb.pos)
+        kv = L.wkv_a(h, xq=hq)                                                      # [T, r + dr]
+        kv_c = C.rms_norm(kv[:, :r].contiguous(), L.kv_norm, cfg.rms_eps) if self.on_gpu else \
+            R.rms_norm(kv[:, :r], L.kv_norm, cfg.rms_eps)
+        k_pe = kv[:, r:].contiguous().view(T, 1, dr)
+        C.rope_(k_pe, 0, dr, self.cos_sin, fb.pos)
+        latent = torch.cat([kv_c.to(self.act_dtype), k_pe.view(T, dr).to(self.act_dtype)], dim=-1)
+        cache.write_latent(i, fb.out_loc, latent)
+        idx_state = None
+        if cfg.use_indexer:
+            idx_state = self.indexer_qkw(i, h, q_lat, fb)
+            cache.write_index_k(i, fb.out_loc, idx_state[1])
+        if fb.is_prefill:
+            o = self._attn_prefill(i, q, kv_c, k_pe, fb, idx_state, cache)
+        else:
+            o = self._attn_decode(i, q, fb, cache, idx_state)
+        return L.wo(o.reshape(T, Hl * dv).to(self.act_dtype).contiguous())
+
+    def indexer_qkw(self, i, h, q_lat, fb):
+        cfg, L = self.cfg, self.layers[i]
+        T, Hi, Di, dr = h.shape[0], cfg.index_n_heads, cfg.index_head_dim, cfg.qk_rope_head_dim
+        q = L.idx_wq(q_lat).view(T, Hi, Di)
+        if not self.on_gpu:
+            q = q.clone()
+        C.rope_(q, 0, dr, self.cos_sin, fb.pos)
+        k = F.layer_norm(L.idx_wk(h).float(), (Di,), L.idx_kn_w, L.idx_kn_b, 1e-6).to(self.act_dtype)
+        k = k.view(T, 1, Di)
+        C.rope_(k, 0, dr, self.cos_sin, fb.pos)
+        w = (L.idx_wp(h, out_dtype=torch.float32) * (Hi ** -0.5) * (Di ** -0.5)).float()
+        return q, k.view(T, Di), w
+
+    def _prefill_key_masks(self, idx_state, fb: ForwardBatch):
+        cfg = self.cfg
+        q, k, w = idx_state
+        masks = []
+        for b in range(len(fb.cu_seqlens) - 1):
+            s, t = fb.cu_seqlens[b], fb.cu_seqlens[b + 1]
+            n = t - s
+            if n <= cfg.index_topk:
+                masks.append(None)
+                continue
+            pos = torch.arange(n, device=q.device)
+            m = torch.zeros(n, n, dtype=torch.bool, device=q.device)
+            for c0 in range(0, n, 512):
+                c1 = min(n, c0 + 512)
+                lg = R.indexer_logits(q[s + c0:s + c1], k[s:t], w[s + c0:s + c1])
+                m[c0:c1] = R.topk_mask(lg, pos[c0:c1], pos, cfg.index_topk)
+            masks.append(m)
+        return masks if any(m is not None for m in masks) else None
+
+    def _attn_prefill(self, i, q, kv_c, k_pe, fb, idx_state, cache):
+        cfg, L = self.cfg, self.layers[i]
+        T, Hl = q.shape[0], self.H_local
+        dn, dr, dv = cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.v_head_dim
+        kvb = L.wkv_b(kv_c.to(self.act_dtype)).view(T, Hl, dn + dv)
+        k = torch.cat([kvb[..., :dn], k_pe.to(kvb.dtype).expand(T, Hl, dr)], dim=-1)
+        v = kvb[..., dn:]
+        masks = self._prefill_key_masks(idx_state, fb) if idx_state is not None else None
+        return A.prefill_attention(q.contiguous(), k.contiguous(), v.contiguous(), fb.cu_seqlens,
+                                   cfg.softmax_scale, masks)
+
+    def _attn_decode(self, i, q, fb, cache, idx_state):
+        cfg, L = self.cfg, self.layers[i]
+        T, Hl = q.shape[0], self.H_local
+        dn, r = cfg.qk_nope_head_dim, cfg.kv_lora_rank
+        q_abs = head_bmm(q[..., :dn], L.w_uk)                                        # [T, Hl, r]
+        qf = torch.cat([q_abs.to(self.act_dtype), q[..., dn:].to(self.act_dtype)], dim=-1).contiguous()
+        idx = fb.key_slots
+        if idx_state is not None and int(fb.key_slots.shape[1]) > cfg.index_topk:
+            qi, _, wi = idx_state
+            idx = A.indexer_topk(qi, wi, cache.index_k[i], fb.key_slots, fb.n_keys, cfg.index_topk)
+        o_lat = A.sparse_mla(qf, cache.latent[i], idx.contiguous(), cfg.softmax_scale, r)   # [T, Hl, r]
+        return head_bmm(o_lat, L.w_uv)                                               # [T, Hl, dv]
+
+    # ------------------------------------------------------------------------------------------------------------------
+    # FFN
+    # ------------------------------------------------------------------------------------------------------------------
+    def ffn(self, i: int, h: torch.Tensor, hq) -> torch.Tensor:
+        cfg, L = self.cfg, self.layers[i]
+        if not L.moe:
+            return L.dense(h, xq=hq)
+        T = h.shape[0]
+        logits = bf16_gemm(h, L.gate_w, out_dtype=torch.float32) if self.on_gpu else h @ L.gate_w.t()
+        w, ids = C.router_topk(logits, L.gate_b, cfg.n_activated_experts, cfg.score_func, cfg.route_scale,
+                               cfg.norm_topk_prob)
+        shared = L.shared(h, xq=hq) if L.shared is not None else None
+        return self.pctx.moe(self, L, h, w, ids, shared)
+
+    def moe_local(self, L, h, w, ids, shared):
+        """All experts local (EP = 1): sort rows by expert, grouped GEMMs, weighted combine."""
+        cfg = self.cfg
+        T, k = ids.shape
+        if not self.on_gpu:
+            out = torch.zeros_like(h)
+            for e in range(self.E_local):
+                rows, slot = torch.nonzero(ids == e, as_tuple=True)
+                if rows.numel() == 0:
+                    continue
+                x = h[rows]
+                y = R.swiglu(x @ L.e_w1[e].t(), x @ L.e_w3[e].t(), cfg.swiglu_limit) @ L.e_w2[e].t()
+                out.index_add_(0, rows, y * w[rows, slot][:, None])
+            return out + shared if shared is not None else out
+        lay = C.MoeLayout(ids, self.E_local)
+        a_q, a_sf = quant_act(h, src_rows=lay.row_src)
+        I2 = 2 * cfg.moe_intermediate
+        act, act_sf = fp8_gemm_swiglu(a_q, a_sf, L.e_w13, cfg.swiglu_limit, lay.m_block_expert, lay.num_blocks, I2)
+        y = fp8_gemm(act, act_sf, L.e_w2, m_block_expert=lay.m_block_expert, num_m_blocks=lay.num_blocks,
+                     n_per_group=cfg.hidden_size)
+        return C.moe_combine(y, w, lay.slot_pos, shared, T)
+
+    # ------------------------------------------------------------------------------------------------------------------
+    # whole model
+    # ------------------------------------------------------------------------------------------------------------------
+    def embed_tokens(self, ids: torch.Tensor):
+        cfg = self.cfg
+        T = ids.shape[0]
+        if not self.on_gpu:
+            X = self.embed[ids.long()][:, None, :].expand(T, cfg.hc_mult, cfg.hidden_size).clone()
+            return X, None
+        return self.pctx.embed(self, ids)
+
+    def forward(self, fb: ForwardBatch, cache) -> torch.Tensor:
+        cfg = self.cfg
+        X, sumsq = self.embed_tokens(fb.ids)
+        for i in range(cfg.n_layers):
+            L = self.layers[i]
+            pre, post, comb = self.hc_coeffs(X, sumsq, L.attn_hc)
+            h, hq = self.pre_norm(X, pre, L.attn_norm, want_fp8=self.on_gpu)
+            a = self.pctx.attn_out(self.attention(i, h, hq, fb, cache))
+            X, sumsq = self.post_mix(X, a, post, comb)
+            pre, post, comb = self.hc_coeffs(X, sumsq, L.ffn_hc)
+            h, hq = self.pre_norm(X, pre, L.ffn_norm, want_fp8=self.on_gpu)
+            f = self.ffn(i, h, hq)
+            X, sumsq = self.post_mix(X, f, post, comb)
+        return self.logits(X, sumsq, fb.logits_rows)
+
+    def logits(self, X, sumsq, rows: Optional[torch.Tensor]) -> torch.Tensor:
+        cfg = self.cfg
+        if rows is not None:
+            X = X[rows.long()].contiguous()
+            sumsq = sumsq[rows.long()] if sumsq is not None else None
+        if not self.on_gpu:
+            pre = R.mhc_head_coeffs(X, self.head_hc.fn, self.head_hc.base, self.head_hc.scale, cfg.hc_eps,
+                                    cfg.rms_eps)
+            y = R.rms_norm(R.mhc_pre_mix(X, pre), self.norm_w, cfg.rms_eps)
+            return y @ self.head_w.w.t()
+        from ..ops._ext import ext
+
+        T = X.shape[0]
+        mix = bf16_gemm(X.view(T, -1), self.head_hc.fn, out_dtype=torch.float32)
+        pre = torch.empty(T, 4, device=X.device)
+        ext().mhc_head_coeffs(mix, sumsq, self.head_hc.base, self.head_hc.scale, X.shape[1] * X.shape[2],
+                              cfg.hc_eps, cfg.rms_eps, pre)
+        y, _ = self.pre_norm(X, pre, self.norm_w, want_fp8=False)
+        return self.pctx.lm_head(self, y)
+
+
+def head_bmm(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    """Per-head matmul: x [T, H, K] · w[h]ᵀ (w [H, N, K]) -> [T, H, N]."""
+    T, H, K = x.shape
+    N = w.shape[1]
+    if not x.is_cuda:
+        return torch.einsum("thk,hnk->thn", x.float(), w.float())
+    Tp = ((T + 127) // 128) * 128
+    xt = torch.zeros(H, Tp, K, dtype=torch.bfloat16, device=x.device)
+    xt[:, :T] = x.transpose(0, 1)
+    mbe = torch.arange(H, dtype=torch.int32, device=x.device).repeat_interleave(Tp // 128)
+    out = bf16_gemm(xt.view(H * Tp, K), w.reshape(H * N, K), m_block_expert=mbe, n_per_group=N)
+    return out.view(H, Tp, N)[:, :T].transpose(0, 1)

@@ -1,0 +1,135 @@
+"""Attention-side ops: MLA prefill (dense causal, optional DSA key mask), absorbed-MLA sparse attention over the
+latent cache, and the DSA lightning indexer with top-k.
+
+Semantics (oracle: ``ref.ops.causal_attention`` / ``indexer_logits`` / ``topk_mask``):
+
+* prefill: q [T,H,dqk], k [T,H,dqk], v [T,H,dv] per sequence (``cu_seqlens``), causal, softmax scale; when
+  ``key_mask`` is given (bool [T, Lmax] per sequence, True = allowed) keys outside the mask are dropped.  This is the
+  DSA "top-k keys per query" rule evaluated inside a dense causal kernel, which for contexts up to a few top-k widths
+  costs fewer FLOPs than the absorbed sparse form.
+* absorbed sparse: q [T,H,dl+dr] against latent rows kv [S, dl+dr] selected by idx [T,K] (-1 = none);
+  o_lat [T,H,dl] = softmax(q·kvᵀ·scale) · kv[:, :dl].  This is the decode / long-context path
+  (reference: ``king_v10/bundle_v9/dec/cuda_decode_attn.py:20-116``, ``cuda_prefill_attn.py:1449``).
+* indexer: logits[t,s] = Σ_h w[t,h]·relu(q[t,h]·k[s]) over each query's causal keys, top-k selection
+  (reference: ``dec/cuda_paged_logits.py:115``, ``cuda_exact_topk.py:559``).
+"""
+from __future__ import annotations
+
+from typing import List, Optional
+
+import torch
+
+from ..ref import ops as R
+from ._ext import ext
+
+
+def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens: List[int], scale: float,
+                      key_masks: Optional[List[Optional[torch.Tensor]]] = None) -> torch.Tensor:
+    T, H, dv = q.shape[0], q.shape[1], v.shape[2]
+    out = torch.empty(T, H, dv, dtype=q.dtype if q.is_cuda else torch.float32, device=q.device)
+    if q.is_cuda:
+        e = ext()
+        if hasattr(e, "attn_prefill"):
+            cu = torch.tensor(cu_seqlens, dtype=torch.int32, device=q.device)
+            mask = None
+            if key_masks is not None and any(m is not None for m in key_masks):
+                mask = pack_key_mask(key_masks, cu_seqlens, q.device)
+            e.attn_prefill(q, k, v, cu, max(b - a for a, b in zip(cu_seqlens[:-1], cu_seqlens[1:])), float(scale),
+                           mask, out)
+            return out
+    for b in range(len(cu_seqlens) - 1):
+        s, t = cu_seqlens[b], cu_seqlens[b + 1]
+        pos = torch.arange(t - s, device=q.device)
+        m = key_masks[b] if key_masks is not None else None
+        if q.is_cuda:
+            # temporary path until the tcgen05 prefill kernel is registered (see attn_prefill)
+            allowed = torch.ones(t - s, t - s, dtype=torch.bool, device=q.device).tril_()
+            if m is not None:
+                allowed &= m
+            o = torch.nn.functional.scaled_dot_product_attention(
+                q[s:t].transpose(0, 1), k[s:t].transpose(0, 1), v[s:t].transpose(0, 1), attn_mask=allowed,
+                scale=scale)
+            out[s:t] = o.transpose(0, 1)
+        else:
+            out[s:t] = R.causal_attention(q[s:t], k[s:t], v[s:t], scale, pos, pos, m)
+    return out
+
+
+def pack_key_mask(key_masks, cu_seqlens, device) -> torch.Tensor:
+    """Per-sequence bool masks -> one uint32 bit matrix [T, ceil(Lmax/32)] (bit j of word w = key 32w+j)."""
+    T = cu_seqlens[-1]
+    Lmax = max(b - a for a, b in zip(cu_seqlens[:-1], cu_seqlens[1:]))
+    W = (Lmax + 31) // 32
+    bits = torch.zeros(T, W * 32, dtype=torch.bool, device=device)
+    for b, m in enumerate(key_masks):
+        s, t = cu_seqlens[b], cu_seqlens[b + 1]
+        if m is None:
+            bits[s:t, : t - s] = True
+        else:
+            bits[s:t, : t - s] = m
+    w = bits.view(T, W, 32).to(torch.int64)
+    shifts = torch.arange(32, device=device, dtype=torch.int64)
+    words = (w << shifts).sum(-1)
+    return words.to(torch.int64).bitwise_and(0xFFFFFFFF).to(torch.int32).contiguous()
+
+
+def sparse_mla(q: torch.Tensor, kv: torch.Tensor, idx: torch.Tensor, scale: float, d_latent: int) -> torch.Tensor:
+    """Absorbed MQA over latent rows: q [T,H,D], kv [S,D], idx [T,K] int32 (-1 pad) -> o_lat [T,H,d_latent]."""
+    T, H, D = q.shape
+    if q.is_cuda:
+        e = ext()
+        if hasattr(e, "sparse_mla"):
+            out = torch.empty(T, H, d_latent, dtype=torch.bfloat16, device=q.device)
+            e.sparse_mla(q, kv, idx, float(scale), out)
+            return out
+        # temporary path until the tcgen05 sparse-MLA kernel is registered
+        sel = kv[idx.clamp(min=0).long()].float()                      # [T, K, D]
+        s = torch.einsum("thd,tkd->thk", q.float(), sel) * scale
+        s = s.masked_fill((idx < 0)[:, None, :], float("-inf"))
+        p = torch.softmax(s, dim=-1)
+        return torch.einsum("thk,tkd->thd", p, sel[..., :d_latent]).to(torch.bfloat16)
+    out = torch.zeros(T, H, d_latent)
+    for t in range(T):
+        sel = idx[t][idx[t] >= 0].long()
+        if sel.numel() == 0:
+            continue
+        keys = kv[sel].float()
+        s = (q[t].float() @ keys.t()) * scale
+        p = torch.softmax(s, dim=-1)
+        out[t] = p @ keys[:, :d_latent]
+    return out
+
+
+def indexer_topk(q: torch.Tensor, w: torch.Tensor, kcache: torch.Tensor, key_slots: torch.Tensor,
+                 n_keys: torch.Tensor, topk: int) -> torch.Tensor:
+    """For each query t: keys are ``key_slots[t, :n_keys[t]]`` (slots of ``kcache``), in causal order.
+    Returns the selected slots [T, topk] (-1 pad), ordered by descending logit (ties -> lower key index)."""
+    T = q.shape[0]
+    if q.is_cuda:
+        e = ext()
+        if hasattr(e, "indexer_topk"):
+            out = torch.empty(T, topk, dtype=torch.int32, device=q.device)
+            e.indexer_topk(q, w, kcache, key_slots, n_keys, out)
+            return out
+        # temporary batched path until the fused indexer kernel is registered (no host sync: graph-capturable)
+        kk = min(topk, key_slots.shape[1])
+        keys = kcache[key_slots.clamp(min=0).long()].float()                       # [T, L, Di]
+        s = torch.einsum("thd,tld->thl", q.float(), keys).clamp_(min=0)
+        logits = torch.einsum("thl,th->tl", s, w.float())
+        valid = torch.arange(key_slots.shape[1], device=q.device)[None, :] < n_keys[:, None]
+        logits = logits.masked_fill(~valid, float("-inf"))
+        top = torch.topk(logits, kk, dim=-1)
+        sel = torch.gather(key_slots, 1, top.indices).masked_fill(torch.isinf(top.values), -1)
+        out = torch.full((T, topk), -1, dtype=torch.int32, device=q.device)
+        out[:, :kk] = sel
+        return out
+    out = torch.full((T, topk), -1, dtype=torch.int32, device=q.device)
+    for t in range(T):
+        n = int(n_keys[t])
+        slots = key_slots[t, :n].long()
+        k = kcache[slots].float()
+        logits = R.indexer_logits(q[t:t + 1].float(), k, w[t:t + 1].float())[0]
+        kk = min(topk, n)
+        order = torch.sort(-logits, stable=True).indices[:kk]
+        out[t, :kk] = slots[order].to(torch.int32)
+    return out

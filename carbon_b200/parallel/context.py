@@ -1,0 +1,56 @@
+"""Parallel context: where the model's collectives plug in.
+
+The model calls four hooks; this module provides the single-rank versions and the NCCL baseline versions.  The
+fused NVLink kernels (``carbon_b200.parallel.fused``) replace the NCCL ones when enabled.
+
+* ``embed(model, ids)``      — vocab-parallel embedding lookup (rows of other ranks come from their HBM).
+* ``attn_out(x)``            — TP attention output reduction (all-reduce of the row-parallel o_proj partials).
+* ``moe(model, L, h, w, ids, shared)`` — expert-parallel MoE: dispatch rows to expert owners, grouped GEMMs, combine.
+* ``lm_head(model, y)``      — vocab-parallel LM head (logits of all ranks' vocabulary shards).
+
+Reference equivalents: MegaMoE's in-kernel dispatch/combine over a symmetric buffer (``cuda_moe_prefill.py:
+4343-4660,5542-5681``), the TP wo_b all-reduce (``slots.py:63``), Engram/embedding peer reads
+(``cuda_peer_read.py:64``).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+
+@dataclass
+class ParallelCtx:
+    rank: int = 0
+    world: int = 1
+    tp: int = 1
+    ep: int = 1
+    tp_rank: int = 0
+    ep_rank: int = 0
+    vocab_parallel: bool = False
+    group: Optional[object] = None   # torch.distributed process group (NCCL) when world > 1
+
+    @staticmethod
+    def single() -> "ParallelCtx":
+        return ParallelCtx()
+
+    # -- hooks (single rank) -----------------------------------------------------------------------------------------
+    def embed(self, model, ids: torch.Tensor):
+        from ..ops._ext import ext
+
+        cfg = model.cfg
+        T = ids.shape[0]
+        X = torch.empty(T, cfg.hc_mult, cfg.hidden_size, dtype=torch.bfloat16, device=ids.device)
+        sumsq = torch.empty(T, device=ids.device)
+        ext().embed_hc(model.embed, model.v_lo, ids.to(torch.int32).contiguous(), X, sumsq)
+        return X, sumsq
+
+    def attn_out(self, x: torch.Tensor) -> torch.Tensor:
+        return x
+
+    def moe(self, model, L, h, w, ids, shared):
+        return model.moe_local(L, h, w, ids, shared)
+
+    def lm_head(self, model, y: torch.Tensor) -> torch.Tensor:
+        return model.head_w(y, out_dtype=torch.float32)
