@@ -1,0 +1,309 @@
+"""Serving benchmark on BASELINE config 5 (full-size DeepSeek-V3/V4-class model, fp8 block-scaled, random init).
+
+    python bench.py --gpus N --steps K --warmup W            # our engine (default N=1)
+    python bench.py --impl reference ...                     # the reference's own build (see --impl reference)
+
+Per GPU (weak scaling; 8 GPUs = the BASELINE config): prefill 4 prompts × 4096 uniform-random token ids per step,
+decode a batch of 32 requests at context 4096 per step (global 32 prompts / batch 256 at N=8).  Timing: W untimed
+warm-up steps, then K steps bracketed by barrier + synchronize, CUDA events on the launching stream, max over
+ranks.  The weights (>100 GB) are far larger than L2, so every step streams them from HBM (no L2 flush needed).
+
+Rank 0 prints one JSON line; `value` is whole-job prefill tokens/s, decode output tokens/s and p50 TPOT are
+extra keys.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "prefill tok/s & decode out tok/s (8×B200, max over ranks); p50 TPOT; roofline %"
+BASELINE_VALUE = None  # BASELINE.md publishes no end-to-end number for this metric
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="deepseek_v3")
+    ap.add_argument("--prompts-per-gpu", type=int, default=4)
+    ap.add_argument("--prompt-len", type=int, default=4096)
+    ap.add_argument("--decode-batch-per-gpu", type=int, default=32)
+    ap.add_argument("--context", type=int, default=4096)
+    ap.add_argument("--decode-steps", type=int, default=16)
+    ap.add_argument("--layers", type=int, default=0, help="override layer count (0 = config's)")
+    ap.add_argument("--mem-frac", type=float, default=0.62, help="HBM fraction for weights (rest: cache, acts)")
+    ap.add_argument("--profile", action="store_true", help="print per-region device times (stderr)")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# clocks sampled during the timed region
+# ----------------------------------------------------------------------------------------------------------------------
+class ClockSampler:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.Q}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                f = [x.strip() for x in out.stdout.strip().split(",")]
+                if len(f) >= 9:
+                    self.samples.append(f)
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[j] for s in self.samples for j in range(4) if "Active" in s[5 + j]
+                          and "Not" not in s[5 + j]})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+def reference_arm(args):
+    """The reference is a set of slot bundles for a sealed SGLang-fork engine (sglang, deep_gemm 0.2.3, FlashMLA,
+    torch 2.14+cu130) gated to sm_103; it has no installable package and cannot run offline here."""
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    why = ("reference is slot bundles for a sealed SGLang-fork engine (needs sglang, deep_gemm 0.2.3.post2, "
+           "FlashMLA; levers gated to sm_103) with no pip-installable package; the install into baseline/_ref "
+           "failed offline")
+    if os.path.isdir(ref_dir) and os.listdir(ref_dir):
+        why = "baseline/_ref holds no importable engine: " + why
+    line = {"impl": "reference", "unavailable": why}
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps(line), flush=True)
+
+
+def pick_layer_sets(cfg, ep: int, mem_bytes: float, frac: float) -> int:
+    """Number of distinct MoE-layer weight sets that fit `frac` of HBM (the rest of the layers reuse them)."""
+    D, E, I = cfg.hidden_size, cfg.n_routed_experts, cfg.moe_intermediate
+    per_moe = (E // ep) * 3 * D * I + 3 * D * I * cfg.n_shared_experts + 300e6
+    dense = cfg.n_dense_layers * (3 * D * cfg.dense_intermediate + 300e6)
+    emb = 2 * cfg.vocab_size * D * 2
+    budget = mem_bytes * frac - dense - emb
+    n_moe = cfg.n_layers - cfg.n_dense_layers
+    return max(1, min(n_moe, int(budget // per_moe)))
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return reference_arm(args)
+    import torch.distributed as dist
+
+    from carbon_b200.config import PRESETS
+    from carbon_b200.engine.engine import Engine
+    from carbon_b200.models.weights import WeightSource
+    from carbon_b200.ops._ext import ext
+    from carbon_b200.parallel.context import ParallelCtx
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+    ext()
+    cfg = PRESETS[args.config]()
+    if args.layers:
+        cfg = cfg.replace(n_layers=args.layers)
+    pctx = ParallelCtx.single() if world == 1 else __import__(
+        "carbon_b200.parallel.ep", fromlist=["make_ctx"]).make_ctx(rank, world)
+    mem = torch.cuda.get_device_properties(dev).total_memory
+    sets = pick_layer_sets(cfg, pctx.ep, mem, args.mem_frac)
+    n_moe = cfg.n_layers - cfg.n_dense_layers
+    tied = sets < n_moe
+    src = WeightSource(cfg, seed=0, layer_sets=sets if tied else None)
+    t0 = time.time()
+    P, S = args.prompts_per_gpu, args.prompt_len
+    B, ctx = args.decode_batch_per_gpu, args.context
+    page = 64
+    pages_needed = (B * ((ctx + args.decode_steps * (args.warmup + args.steps) + 2 * page) // page + 1) +
+                    P * (S // page + 2) + 8)
+    eng = Engine(cfg, device=dev, source=src, num_pages=pages_needed, page_size=page, cuda_graphs=True,
+                 graph_buckets=(B,), pctx=pctx)
+    torch.cuda.synchronize()
+    init_s = time.time() - t0
+    gen = torch.Generator().manual_seed(1234 + rank)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    # ---------------- prefill (device-timed) ----------------
+    def prefill_step():
+        reqs = [eng.add_request(torch.randint(0, cfg.vocab_size, (S,), generator=gen).tolist()) for _ in range(P)]
+        logits = eng.prefill(reqs)
+        for r in reqs:
+            eng.release(r)
+        return logits
+
+    for _ in range(args.warmup):
+        prefill_step()
+    barrier()
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    with ClockSampler(local) as clk:
+        ev[0].record()
+        for _ in range(args.steps):
+            prefill_step()
+        ev[1].record()
+        barrier()
+    pf_ms = ev[0].elapsed_time(ev[1]) / args.steps
+    pf_ms = max_over_ranks(pf_ms, world)
+
+    # ---------------- prefill end to end through the public API (H2D ids from pinned host, D2H next tokens) ------
+    host_ids = [torch.randint(0, cfg.vocab_size, (S,), generator=gen).pin_memory() for _ in range(P)]
+    barrier()
+    ee = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ee[0].record()
+    d2h = 0
+    for _ in range(args.steps):
+        reqs = [eng.add_request(h.tolist()) for h in host_ids]
+        nxt = torch.argmax(eng.prefill(reqs), dim=-1).cpu()
+        d2h += nxt.numel() * nxt.element_size()
+        for r in reqs:
+            eng.release(r)
+    ee[1].record()
+    barrier()
+    e2e_ms = max_over_ranks(ee[0].elapsed_time(ee[1]) / args.steps, world)
+
+    # ---------------- decode (CUDA graphs, context `ctx`) ----------------
+    reqs = []
+    for _ in range(B):
+        r = eng.add_request(torch.randint(0, cfg.vocab_size, (ctx,), generator=gen).tolist())
+        eng._ensure_pages(r, r.seq_len)
+        r.n_cached = ctx          # cache rows are synthetic: decode cost depends on context length, not content
+        reqs.append(r)
+    nxt = [1] * B
+    for _ in range(args.warmup):
+        for _ in range(2):
+            eng.decode(reqs, nxt)
+    barrier()
+    step_ms = []
+    for _ in range(args.steps):
+        for _ in range(args.decode_steps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            eng.decode(reqs, nxt)
+            b.record()
+            step_ms.append((a, b))
+    barrier()
+    tp = [a.elapsed_time(b) for a, b in step_ms]
+    dec_ms = max_over_ranks(sum(tp) / len(tp), world)
+    tpot_p50 = max_over_ranks(statistics.median(tp), world)
+
+    launches = count_launches(eng, P, S)
+    if args.profile and rank == 0:
+        from carbon_b200.utils.trace import tracing
+
+        with tracing() as t:
+            prefill_step()
+        print("== prefill regions ==\n" + t.table(), file=sys.stderr, flush=True)
+        eng.cuda_graphs = False
+        with tracing() as t:
+            eng.decode(reqs, nxt)
+        eng.cuda_graphs = True
+        print("== decode regions (eager) ==\n" + t.table(), file=sys.stderr, flush=True)
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        pf_tok_s = P * S * world / (pf_ms / 1e3)
+        line = {
+            "metric": METRIC, "value": round(pf_tok_s, 1), "unit": "tokens/s (prefill, whole job)",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(pf_ms, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp8 weights+GEMM inputs, "
+            "bf16 activations", "data": "synthetic uniform-random token ids; random-init weights (N(0,0.02))",
+            "decode_out_tok_s": round(B * world / (dec_ms / 1e3), 1), "tpot_p50_ms": round(tpot_p50, 3),
+            "decode_ms_per_step": round(dec_ms, 3),
+            "e2e": {"value": round(P * S * world / (e2e_ms / 1e3), 1), "unit": "tokens/s (prefill via Engine.prefill)",
+                    "h2d_bytes_per_step": P * S * 4, "d2h_bytes_per_step": d2h // max(args.steps, 1)},
+            "gpu_launches": launches,
+            "clocks": clk.summary(),
+            "config": {"model": f"{args.config} ({cfg.n_layers} layers, hidden {cfg.hidden_size}, "
+                                f"{cfg.n_routed_experts} experts top-{cfg.n_activated_experts})",
+                       "global_batch": P * world, "seq_len": S, "decode_batch": B * world, "context": ctx,
+                       "parallelism": pctx_name(pctx, world),
+                       "weights": (f"{sets} distinct MoE-layer weight sets cycled over {n_moe} MoE layers "
+                                   "(every layer still runs; the full untied model needs 8 GPUs)") if tied
+                       else "all layers distinct", "l2": "inputs (weights) larger than L2",
+                       "init_s": round(init_s, 1)},
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def pctx_name(p, world):
+    return "single GPU" if world == 1 else f"tp{p.tp}-ep{p.ep}"
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch.distributed as dist
+
+    t = torch.tensor([v], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def count_launches(eng, P, S) -> int:
+    """Kernel launches of this repo's extension during one prefill step (counted by the bindings)."""
+    from carbon_b200.ops._ext import ext
+
+    e = ext()
+    if not hasattr(e, "launch_count"):
+        return 0
+    reqs = [eng.add_request([1] * S) for _ in range(P)]
+    torch.cuda.synchronize()
+    c0 = e.launch_count()
+    eng.prefill(reqs)
+    torch.cuda.synchronize()
+    c1 = e.launch_count()
+    for r in reqs:
+        eng.release(r)
+    return int(c1 - c0)
+
+
+if __name__ == "__main__":
+    main()

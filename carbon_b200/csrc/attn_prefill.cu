@@ -1,0 +1,353 @@
+// MLA prefill attention on tcgen05 (sm_100a): O = softmax(Q·Kᵀ·scale, causal [+ DSA key mask])·V
+// per (sequence, head, 128-query tile).  Q/K head dim 192 (= 128 nope + 64 rope), V head dim 128, bf16 in/out.
+//
+// CTA roles (256 threads):
+//   warp 0  TMA: Q once, then K tiles into a 2-deep ring          warp 3  TMA: V tiles (1 stage)
+//   warp 1  MMA: S[j%2] = Q·K_jᵀ (TMEM), O += P_j·V_j (TMEM)        warp 2  TMEM allocator
+//   warps 4-7 softmax: one query row per thread; S from TMEM, P (bf16) to shared memory in the 128B-swizzled
+//            K-major layout the MMA reads, lazy rescale of O in TMEM (only when the row max grows by > 2^8),
+//            final O/l to global.
+// TMEM: S0 cols [0,128), S1 [128,256), O [256,384).
+// Shared memory: Q 48 KB | K 2 x 48 KB | V 32 KB | P 32 KB  (= 208 KB) + barriers.
+//
+// The DSA variant passes a bit matrix mask[T, W] (bit j of word w = key 32w+j of the query's sequence allowed):
+// the indexer's top-k selection is applied inside the dense causal tile loop.  Reference kernel with the same
+// role: the FlashMLA-derived sparse prefill (king_v10/bundle_v9/cuda_prefill_attn.py:1449), whose head layout
+// (latent MQA 64x512) differs from this model's MLA (128 heads, 192/128).
+#include <cudaTypedefs.h>
+#include "ptx.cuh"
+
+namespace cb {
+
+bool make_tmap_2d(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+                  uint64_t rows, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_rows,
+                  CUtensorMapSwizzle swz);
+
+namespace fa {
+
+constexpr int BM = 128, BN = 128, DQK = 192, DV = 128;
+constexpr int Q_BYTES = BM * DQK * 2;          // 48 KB (3 swizzle atoms of 64 dims)
+constexpr int K_BYTES = BN * DQK * 2;          // 48 KB
+constexpr int V_BYTES = BN * DV * 2;           // 32 KB (2 atoms of 64 dims)
+constexpr int P_BYTES = BM * BN * 2;           // 32 KB (2 atoms of 64 keys)
+constexpr int ATOM = 128 * 128;                // bytes of one [128 rows x 128 B] swizzled box
+constexpr int SMEM = 1024 + Q_BYTES + 2 * K_BYTES + V_BYTES + P_BYTES + 256;
+constexpr float kRescaleThresh = 8.0f;         // log2 units
+
+struct Params {
+  const int4* tiles;      // [n_tiles] (seq_start, seq_len, q0, unused)
+  const uint32_t* mask;   // optional [T, mask_words]
+  int mask_words;
+  int H;
+  float scale_log2;       // softmax scale * log2(e)
+  __nv_bfloat16* out;     // [T, H, DV]
+  int* status;
+};
+
+// MN-major (V as the B operand, N = dv contiguous) 128B-swizzled descriptor: LBO = bytes between 64-wide dv
+// atoms, SBO = bytes between 8-row key groups.
+CB_DEVICE uint64_t desc_mn_sw128(const void* p, uint32_t lbo, uint32_t sbo) {
+  const uint64_t addr = smem_u32(p);
+  uint64_t d = 0;
+  d |= (addr >> 4) & 0x3FFFull;
+  d |= uint64_t((lbo >> 4) & 0x3FFF) << 16;
+  d |= uint64_t((sbo >> 4) & 0x3FFF) << 32;
+  d |= uint64_t(1) << 46;
+  d |= uint64_t(2) << 61;
+  return d;
+}
+
+CB_HOST_DEVICE uint32_t idesc_bf16_bmn(int M, int N) {  // A K-major, B MN-major
+  return idesc_bf16(M, N) | (1u << 16);
+}
+
+__global__ void __launch_bounds__(256, 1) attn_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
+                                                              const __grid_constant__ CUtensorMap tm_k,
+                                                              const __grid_constant__ CUtensorMap tm_v,
+                                                              const Params p) {
+#if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 1000
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + Q_BYTES;                 // 2 stages
+  uint8_t* sV = sK + 2 * K_BYTES;
+  uint8_t* sP = sV + V_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + P_BYTES);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;    // [2]
+  uint64_t* k_empty = bars + 3;   // [2]
+  uint64_t* v_full = bars + 5;
+  uint64_t* v_empty = bars + 6;
+  uint64_t* s_full = bars + 7;    // [2]
+  uint64_t* s_empty = bars + 9;   // [2]
+  uint64_t* p_full = bars + 11;
+  uint64_t* pv_done = bars + 12;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int4 tile = p.tiles[blockIdx.x];
+  const int seq_start = tile.x, seq_len = tile.y, q0 = tile.z;
+  const int h = blockIdx.y;
+  const int q_end = min(q0 + BM, seq_len);
+  const int n_kt = (q_end + BN - 1) / BN;     // causal: keys [0, q_end)
+
+  const uint32_t warp = warp_id(), lane = lane_id();
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1);
+                                  mbar_init(&s_full[i], 1); mbar_init(&s_empty[i], 128); }
+    mbar_init(v_full, 1); mbar_init(v_empty, 1); mbar_init(p_full, 128); mbar_init(pv_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto fail = [&](int code) { if (p.status) atomicCAS(p.status, 0, code); *abort_flag = 1; };
+
+  if (warp == 0) {
+    if (elect_one()) {
+      tma_prefetch_desc(&tm_q); tma_prefetch_desc(&tm_k);
+      mbar_arrive_expect_tx(q_full, Q_BYTES);
+      for (int a = 0; a < 3; ++a) tma_load_3d(sQ + a * ATOM, &tm_q, q_full, a * 64, h, seq_start + q0);
+      for (int j = 0; j < n_kt && !*abort_flag; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&k_empty[s], ((j >> 1) & 1) ^ 1)) { fail(kErrTimeoutEmpty); break; }
+        mbar_arrive_expect_tx(&k_full[s], K_BYTES);
+        for (int a = 0; a < 3; ++a)
+          tma_load_3d(sK + s * K_BYTES + a * ATOM, &tm_k, &k_full[s], a * 64, h, seq_start + j * BN);
+      }
+    }
+  } else if (warp == 3) {
+    if (elect_one()) {
+      tma_prefetch_desc(&tm_v);
+      for (int j = 0; j < n_kt && !*abort_flag; ++j) {
+        if (!mbar_wait(v_empty, (j & 1) ^ 1)) { fail(kErrTimeoutEmpty); break; }
+        mbar_arrive_expect_tx(v_full, V_BYTES);
+        for (int a = 0; a < 2; ++a) tma_load_3d(sV + a * ATOM, &tm_v, v_full, a * 64, h, seq_start + j * BN);
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      const uint32_t id_qk = idesc_bf16(BM, BN);
+      const uint32_t id_pv = idesc_bf16_bmn(BM, DV);
+      bool ok = mbar_wait(q_full, 0);
+      if (!ok) fail(kErrTimeoutFull);
+      auto issue_qk = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(&k_full[s], (j >> 1) & 1)) { fail(kErrTimeoutFull); return false; }
+        if (!mbar_wait(&s_empty[s], ((j >> 1) & 1) ^ 1)) { fail(kErrTimeoutTmem); return false; }
+        tc_fence_after();
+        for (int k = 0; k < DQK / 16; ++k) {
+          const int a = k >> 2, off = (k & 3) * 32;
+          mma_f16_ss(tmem + s * 128, smem_desc_sw128(sQ + a * ATOM + off),
+                     smem_desc_sw128(sK + s * K_BYTES + a * ATOM + off), id_qk, k > 0);
+        }
+        mma_commit(&s_full[s]);
+        mma_commit(&k_empty[s]);
+        return true;
+      };
+      auto issue_pv = [&](int j) -> bool {
+        if (!mbar_wait(p_full, j & 1)) { fail(kErrTimeoutFull); return false; }
+        if (!mbar_wait(v_full, j & 1)) { fail(kErrTimeoutFull); return false; }
+        tc_fence_after();
+        for (int k = 0; k < BN / 16; ++k) {
+          // A = P (K-major, keys along K): atom k/4, 32-byte step inside the atom
+          const uint64_t a_desc = smem_desc_sw128(sP + (k >> 2) * ATOM + (k & 3) * 32);
+          // B = V (MN-major): 16 keys = 16 rows of 128 B
+          const uint64_t b_desc = desc_mn_sw128(sV + k * 16 * 128, ATOM, 1024);
+          mma_f16_ss(tmem + 256, a_desc, b_desc, id_pv, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        mma_commit(pv_done);
+        mma_commit(v_empty);
+        return true;
+      };
+      if (ok) ok = issue_qk(0);
+      for (int j = 0; ok && j < n_kt && !*abort_flag; ++j) {
+        if (j + 1 < n_kt) ok = issue_qk(j + 1);
+        if (ok) ok = issue_pv(j);
+      }
+    }
+  } else if (warp >= 4) {
+    // ---------------- softmax / correction / epilogue ----------------
+    const uint32_t q = warp & 3;
+    const int row = q * 32 + lane;               // query row within the tile
+    const int qi = q0 + row;                     // query index within the sequence
+    const int tok = seq_start + qi;
+    const uint32_t t_lane = tmem + ((q * 32) << 16);
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kt; ++j) {
+      const int s = j & 1;
+      if (!mbar_wait(&s_full[s], (j >> 1) & 1)) { fail(kErrTimeoutTmem); ok = false; break; }
+      tc_fence_after();
+      float sv[BN];
+#pragma unroll
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_lane + s * 128 + c, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sv[c + i] = __uint_as_float(r[i]);
+      }
+      tc_fence_before();
+      mbar_arrive(&s_empty[s]);
+      // mask + scale (log2 domain)
+      const int k0 = j * BN;
+      float mt = -INFINITY;
+      uint32_t words[BN / 32];
+#pragma unroll
+      for (int w = 0; w < BN / 32; ++w)
+        words[w] = (p.mask && qi < seq_len && (k0 / 32 + w) < p.mask_words)
+                       ? p.mask[size_t(tok) * p.mask_words + k0 / 32 + w] : 0xffffffffu;
+#pragma unroll
+      for (int i = 0; i < BN; ++i) {
+        const int kk = k0 + i;
+        const bool allowed = kk <= qi && ((words[i >> 5] >> (i & 31)) & 1u);
+        sv[i] = allowed ? sv[i] * p.scale_log2 : -INFINITY;
+        mt = fmaxf(mt, sv[i]);
+      }
+      // lazy rescale
+      bool need = (j > 0) && (mt > m_used + kRescaleThresh);
+      const float m_new = need || j == 0 ? fmaxf(m_used, mt) : m_used;
+      const float m_ref = m_new == -INFINITY ? 0.f : m_new;
+      float alpha = 1.f;
+      if (need && m_used != -INFINITY) alpha = exp2f(m_used - m_ref);
+      float rs = 0.f;
+      uint32_t pk[BN / 2];
+#pragma unroll
+      for (int i = 0; i < BN; i += 2) {
+        const float a = exp2f(sv[i] - m_ref), b = exp2f(sv[i + 1] - m_ref);
+        rs += a + b;
+        pk[i / 2] = pack_bf16x2(a, b);
+      }
+      l = l * alpha + rs;
+      m_used = m_new;
+      // wait for the previous P·V (it reads P and accumulates into O)
+      if (j > 0) {
+        if (!mbar_wait(pv_done, (j - 1) & 1)) { fail(kErrTimeoutTmem); ok = false; break; }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+          for (int c = 0; c < DV; c += 16) {
+            uint32_t r[16];
+            tmem_ld_32x32b_x16(t_lane + 256 + c, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+            tmem_st_32x32b_x16(t_lane + 256 + c, r);
+          }
+          tmem_st_wait();
+        }
+      }
+      // P row -> shared memory (two 64-key swizzle atoms)
+#pragma unroll
+      for (int c = 0; c < 16; ++c) {
+        uint8_t* dst = sP + (c >> 3) * ATOM + row * 128 + ((((c & 7) ^ (row & 7))) << 4);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && n_kt > 0) {
+      if (!mbar_wait(pv_done, (n_kt - 1) & 1)) { fail(kErrTimeoutTmem); ok = false; }
+    }
+    if (ok) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* o = p.out + (size_t(tok) * p.H + h) * DV;
+#pragma unroll 1
+      for (int c = 0; c < DV; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_lane + 256 + c, r);
+        tmem_ld_wait();
+        if (qi < seq_len) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]) * inv, __uint_as_float(r[8 * v + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]) * inv, __uint_as_float(r[8 * v + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * inv, __uint_as_float(r[8 * v + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * inv, __uint_as_float(r[8 * v + 7]) * inv);
+            reinterpret_cast<uint4*>(o + c)[v] = w;
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 2) { tc_fence_after(); tmem_dealloc(tmem, 512); }
+#endif
+}
+
+static bool make_tmap_3d(CUtensorMap* m, const void* ptr, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
+                         uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2);
+
+}  // namespace fa
+
+// Host: q [T,H,192], k [T,H,192], v [T,H,128] bf16 contiguous; tiles [n_tiles] int4; out [T,H,128].
+cudaError_t attn_prefill(const void* q, const void* k, const void* v, int T, int H, const int* tiles, int n_tiles,
+                         const uint32_t* mask, int mask_words, float scale, void* out, int* status, cudaStream_t s);
+
+}  // namespace cb
+
+// ---------------------------------------------------------------------------------------------------------------
+namespace cb {
+namespace fa {
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+static bool make_tmap_3d(CUtensorMap* m, const void* ptr, uint64_t d0, uint64_t d1, uint64_t d2, uint64_t s1,
+                         uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2) {
+  auto fn = encode_fn();
+  if (!fn || (reinterpret_cast<uintptr_t>(ptr) & 15) || (s1 & 15) || (s2 & 15)) return false;
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {s1, s2};
+  cuuint32_t box[3] = {b0, b1, b2};
+  cuuint32_t es[3] = {1, 1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(ptr), dims, strides, box, es,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+}  // namespace fa
+
+cudaError_t attn_prefill(const void* q, const void* k, const void* v, int T, int H, const int* tiles, int n_tiles,
+                         const uint32_t* mask, int mask_words, float scale, void* out, int* status, cudaStream_t s) {
+  using namespace fa;
+  if (n_tiles == 0) return cudaSuccess;
+  CUtensorMap tq, tk, tv;
+  if (!make_tmap_3d(&tq, q, DQK, H, T, DQK * 2, uint64_t(H) * DQK * 2, 64, 1, BM) ||
+      !make_tmap_3d(&tk, k, DQK, H, T, DQK * 2, uint64_t(H) * DQK * 2, 64, 1, BN) ||
+      !make_tmap_3d(&tv, v, DV, H, T, DV * 2, uint64_t(H) * DV * 2, 64, 1, BN))
+    return cudaErrorInvalidValue;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  Params p;
+  p.tiles = reinterpret_cast<const int4*>(tiles);
+  p.mask = mask;
+  p.mask_words = mask_words;
+  p.H = H;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.status = status;
+  dim3 grid(n_tiles, H);
+  attn_prefill_kernel<<<grid, 256, SMEM, s>>>(tq, tk, tv, p);
+  return cudaGetLastError();
+}
+
+}  // namespace cb

@@ -2,6 +2,7 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <atomic>
 #include "small_ops.h"
 
 namespace {
@@ -9,10 +10,13 @@ namespace {
 #define CHECK_CUDA(t) TORCH_CHECK((t).is_cuda(), #t " must be a CUDA tensor")
 #define CHECK_CONTIG(t) TORCH_CHECK((t).is_contiguous(), #t " must be contiguous")
 #define CHECK_DT(t, d) TORCH_CHECK((t).scalar_type() == (d), #t " has dtype ", (t).scalar_type(), ", expected ", (d))
+std::atomic<int64_t> g_launches{0};   // kernels launched through these bindings (bench.py reports it)
+
 #define CK(expr)                                                                          \
   do {                                                                                    \
     cudaError_t _e = (expr);                                                              \
     TORCH_CHECK(_e == cudaSuccess, #expr " failed: ", cudaGetErrorString(_e));            \
+    g_launches.fetch_add(1, std::memory_order_relaxed);                                   \
   } while (0)
 
 cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
@@ -210,6 +214,41 @@ void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor out, int64_t epi,
                    grouped ? m_block_expert->numel() : 0, ptr_or_null<int>(status), num_sms(), cur_stream()));
 }
 
+void attn_prefill(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor tiles,
+                  c10::optional<torch::Tensor> mask, double scale, torch::Tensor out,
+                  c10::optional<torch::Tensor> status) {
+  CHECK_CUDA(q); CHECK_DT(q, at::kBFloat16); CHECK_DT(k, at::kBFloat16); CHECK_DT(v, at::kBFloat16);
+  CHECK_CONTIG(q); CHECK_CONTIG(k); CHECK_CONTIG(v); CHECK_CONTIG(out); CHECK_DT(tiles, at::kInt);
+  TORCH_CHECK(q.size(2) == 192 && k.size(2) == 192 && v.size(2) == 128, "attn_prefill: head dims 192/128");
+  TORCH_CHECK(tiles.dim() == 2 && tiles.size(1) == 4);
+  const int T = q.size(0), H = q.size(1);
+  int words = 0;
+  if (mask.has_value()) { CHECK_DT((*mask), at::kInt); TORCH_CHECK(mask->size(0) == T); words = mask->size(1); }
+  c10::cuda::CUDAGuard g(q.device());
+  CK(cb::attn_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), T, H, tiles.data_ptr<int>(), tiles.size(0),
+                      ptr_or_null<const uint32_t>(mask), words, float(scale), out.data_ptr(),
+                      ptr_or_null<int>(status), cur_stream()));
+}
+
+// keys [L, Di] bf16, q [Tq, H, Di] bf16, w [Tq, H] fp32 -> logits [Tq, ldo] fp32
+void indexer_logits(torch::Tensor keys, torch::Tensor q, torch::Tensor w, torch::Tensor out, bool causal) {
+  CHECK_CUDA(keys); CHECK_DT(keys, at::kBFloat16); CHECK_DT(q, at::kBFloat16); CHECK_DT(w, at::kFloat);
+  CHECK_CONTIG(keys); CHECK_CONTIG(q); CHECK_CONTIG(w); CHECK_DT(out, at::kFloat);
+  TORCH_CHECK(out.stride(1) == 1 && out.size(0) >= q.size(0) && out.stride(0) >= keys.size(0));
+  c10::cuda::CUDAGuard g(keys.device());
+  CK(cb::indexer_logits(keys.data_ptr(), keys.size(0), q.data_ptr(), q.size(0), q.size(1), q.size(2),
+                        w.data_ptr<float>(), out.data_ptr<float>(), out.stride(0), causal, nullptr, num_sms(),
+                        cur_stream()));
+}
+
+void topk_mask(torch::Tensor logits, int64_t Tq, int64_t k, torch::Tensor mask, int64_t row0) {
+  CHECK_CUDA(logits); CHECK_DT(logits, at::kFloat); CHECK_DT(mask, at::kInt); CHECK_CONTIG(mask);
+  TORCH_CHECK(logits.stride(1) == 1 && row0 + Tq <= mask.size(0) && mask.size(1) * 32 >= Tq);
+  c10::cuda::CUDAGuard g(logits.device());
+  CK(cb::topk_mask(logits.data_ptr<float>(), logits.stride(0), Tq, k, reinterpret_cast<uint32_t*>(mask.data_ptr()),
+                   mask.size(1), row0, cur_stream()));
+}
+
 }  // namespace
 
 void register_runtime(pybind11::module_& m);
@@ -233,4 +272,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_fp8", &gemm_fp8);
   m.def("gemm_bf16", &gemm_bf16);
   m.def("sf_words", &sf_words);
+  m.def("launch_count", []() { return g_launches.load(); });
+  m.def("attn_prefill", &attn_prefill);
+  m.def("indexer_logits", &indexer_logits);
+  m.def("topk_mask", &topk_mask);
 }

@@ -102,4 +102,24 @@ cudaError_t gemm_bf16(const void* A, int lda, const void* B, int ldb, int M, int
   return launch<KIND_BF16, EPI_BF16, 128, 6, 2>(ta, tb, p, max_tiles, num_sms, s);
 }
 
+// DSA indexer logits: keys [L, Di] bf16, q [Tq*H, Di] bf16, w [Tq, H] fp32 -> logits [Tq, ldo] fp32 (causal).
+cudaError_t indexer_logits(const void* keys, int L, const void* q, int Tq, int H, int Di, const float* w, float* out,
+                           int ldo, bool causal, int* status, int num_sms, cudaStream_t s) {
+  if (L <= 0 || Tq <= 0) return cudaSuccess;
+  constexpr int BN = 256;
+  if (Di % 64 || BN % H || H % 32) return cudaErrorInvalidValue;
+  CUtensorMap ta, tb;
+  if (!make_tmap_2d(&ta, keys, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Di, L, uint64_t(Di) * 2, 64, 128,
+                    CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tmap_2d(&tb, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Di, uint64_t(Tq) * H, uint64_t(Di) * 2, 64, BN,
+                    CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  GemmParams p{};
+  p.M = L; p.N = Tq * H; p.K = Di;
+  p.out = out; p.ldo = ldo; p.status = status;
+  p.idx_w = w; p.idx_heads = H; p.causal = causal ? 1 : 0;
+  const int max_tiles = ceil_div(L, 128) * ceil_div(Tq * H, BN);
+  return launch<KIND_BF16, EPI_INDEXER, 256, 4, 2>(ta, tb, p, max_tiles, num_sms, s);
+}
+
 }  // namespace cb

@@ -21,7 +21,7 @@
 namespace cb {
 
 enum GemmKind { KIND_MXF8 = 0, KIND_BF16 = 1 };
-enum GemmEpi { EPI_BF16 = 0, EPI_SWIGLU_FP8 = 1, EPI_F32 = 2 };
+enum GemmEpi { EPI_BF16 = 0, EPI_SWIGLU_FP8 = 1, EPI_F32 = 2, EPI_INDEXER = 3 };
 
 struct GemmParams {
   int M, N, K;                 // N = per-expert N in grouped mode
@@ -36,6 +36,11 @@ struct GemmParams {
   const int* m_block_expert;   // grouped: expert of each 128-row block (or -1); nullptr = dense
   const int* num_m_blocks_dev; // grouped: number of valid m blocks (device), nullptr => ceil(M/128)
   int* status;                 // error word (0 = ok)
+  // EPI_INDEXER (DSA lightning indexer): A = keys [L, Di], B = queries x heads [Tq*H, Di]; the epilogue writes
+  // logits[q, key] = sum_h w[q, h] * relu(acc[key, q*H + h]) (fp32, row stride ldo), -inf for key > q (causal).
+  const float* idx_w;          // [Tq, idx_heads]
+  int idx_heads;
+  int causal;                  // skip tiles whose first key is after their last query
 };
 
 template <int BLOCK_N>
@@ -118,6 +123,15 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
     if (p.status) atomicCAS(p.status, 0, code);
     *abort_flag = 1;
   };
+  // causal tile skip (indexer): queries of tile nb are [nb*QPT, nb*QPT+QPT)
+  auto skip_tile = [&](int mb, int nb) -> bool {
+    if constexpr (EPI == EPI_INDEXER) {
+      const int qpt = BLOCK_N / p.idx_heads;
+      return p.causal && mb * BLOCK_M > nb * qpt + qpt - 1;
+    } else {
+      return false;
+    }
+  };
 
   if (warp == 0) {
     // ================= TMA producer =================
@@ -125,6 +139,7 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
       int stage = 0; uint32_t phase = 0;
       for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
         int mb, nb; tile_coords(t, mb, nb);
+        if (skip_tile(mb, nb)) continue;
         int expert = 0;
         if (grouped) { expert = p.m_block_expert[mb]; if (expert < 0) continue; }
         const int a_row = mb * BLOCK_M;
@@ -153,6 +168,7 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
       int stage = 0; uint32_t phase = 0; int iter = 0;
       for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
         int mb, nb; tile_coords(t, mb, nb);
+        if (skip_tile(mb, nb)) continue;
         if (grouped && p.m_block_expert[mb] < 0) continue;
         const int acc = iter % ACC_STAGES;
         const uint32_t acc_phase = (iter / ACC_STAGES) & 1;
@@ -200,6 +216,7 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
     int iter = 0;
     for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
       int mb, nb; tile_coords(t, mb, nb);
+      if (skip_tile(mb, nb)) continue;
       if (grouped && p.m_block_expert[mb] < 0) continue;
       const int acc = iter % ACC_STAGES;
       const uint32_t acc_phase = (iter / ACC_STAGES) & 1;
@@ -241,6 +258,27 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
                 for (int j = 0; j < 32 && col0 + j < p.N; ++j) o[j] = __uint_as_float(v[j]);
               }
             }
+          }
+        }
+      } else if constexpr (EPI == EPI_INDEXER) {
+        const int qpt = BLOCK_N / p.idx_heads;
+        const int key = row;                                   // A rows are keys
+        for (int j = 0; j < qpt; ++j) {
+          const int qi = nb * qpt + j;
+          const bool q_ok = qi * p.idx_heads < p.N;
+          const float* wq = p.idx_w + size_t(q_ok ? qi : 0) * p.idx_heads;
+          float acc_l = 0.f;
+#pragma unroll 1
+          for (int c = 0; c < p.idx_heads; c += 32) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(t_row + j * p.idx_heads + c, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc_l += wq[c + i] * fmaxf(__uint_as_float(v[i]), 0.f);
+          }
+          if (row_ok && q_ok) {
+            float* o = reinterpret_cast<float*>(p.out) + size_t(qi) * p.ldo + key;
+            *o = (p.causal && key > qi) ? -INFINITY : acc_l;
           }
         }
       } else {

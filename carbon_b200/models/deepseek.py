@@ -29,6 +29,7 @@ from ..ops import core as C
 from ..ops.gemm import bf16_gemm, fp8_gemm, fp8_gemm_swiglu, interleave_gate_up
 from ..ops.quant import Fp8Weight, quant_act, quantize_weight, stack_weights
 from ..ref import ops as R
+from ..utils.trace import region
 from .weights import WeightSource
 
 
@@ -130,6 +131,7 @@ class DeepseekModel:
         self.on_gpu = self.device.type == "cuda"
         self.pctx = pctx if pctx is not None else ParallelCtx.single()
         self.fp8 = fp8
+        self.trace = None          # set to a list to record (name, tensor) at sublayer boundaries (debugging)
         cfg.validate()
         tp, ep = self.pctx.tp, self.pctx.ep
         self.H_local = cfg.n_heads // tp
@@ -147,7 +149,15 @@ class DeepseekModel:
         self.head_w = Lin(get("head.weight", slice(self.v_lo, self.v_hi)), dev, fp8=False)
         self.head_hc = make_hc(get("head_hc.fn"), get("head_hc.base"), get("head_hc.scale"), dev)
         self.norm_w = get("norm.weight")
-        self.layers = [self._load_layer(i, get) for i in range(cfg.n_layers)]
+        # layers whose weights are tied (WeightSource.layer_sets) share one Layer object
+        built: Dict[str, Layer] = {}
+        self.layers = []
+        for i in range(cfg.n_layers):
+            key = source.canonical(f"layers.{i}.")
+            if key not in built:
+                built[key] = self._load_layer(i, get)
+            self.layers.append(built[key])
+        self.n_weight_sets = len(built)
 
     # ------------------------------------------------------------------------------------------------------------------
     def _load_layer(self, i: int, get) -> Layer:
@@ -172,7 +182,8 @@ class DeepseekModel:
         L.kv_norm = get(a + "kv_norm.weight")
         wkv_b = get(a + "wkv_b.weight", slice(h0 * (dn + dv), h1 * (dn + dv)))      # [Hl*(dn+dv), r]
         L.wkv_b = Lin(wkv_b, dev, self.fp8)
-        wkv_b3 = wkv_b.view(Hl, dn + dv, r)
+        # absorbed decode uses the same (fp8-rounded) wkv_b as the prefill GEMM
+        wkv_b3 = (L.wkv_b.fw.dequant() if L.wkv_b.kind == "fp8" else wkv_b).view(Hl, dn + dv, r)
         L.w_uk = wkv_b3[:, :dn, :].transpose(1, 2).contiguous().to(self.act_dtype)  # [Hl, r, dn]: q_abs = q_nope·w_ukᵀ
         L.w_uv = wkv_b3[:, dn:, :].contiguous().to(self.act_dtype)                  # [Hl, dv, r]
         wo = get(a + "wo.weight")                                                  # [D, H*dv]
@@ -190,7 +201,7 @@ class DeepseekModel:
         else:
             E, El = cfg.n_routed_experts, self.E_local
             e0 = pc.ep_rank * El
-            L.gate_w = get(f + "gate.weight").to(self.act_dtype).contiguous()
+            L.gate = Lin(get(f + "gate.weight"), dev, fp8=False)
             L.gate_b = get(f + "gate.bias")
             if dev.type == "cpu":
                 L.e_w1 = get(f + "experts.w1", slice(e0, e0 + El))
@@ -263,35 +274,39 @@ class DeepseekModel:
         cfg, L = self.cfg, self.layers[i]
         T, Hl = h.shape[0], self.H_local
         dn, dr, dv, r = cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.v_head_dim, cfg.kv_lora_rank
-        if cfg.q_lora_rank > 0:
-            q_lat_raw = L.wq_a(h, xq=hq)
-            if self.on_gpu:
-                q_lat, q_lat_q = C.rms_norm(q_lat_raw, L.q_norm, cfg.rms_eps, want_bf16=True, want_fp8=True)
+        with region("attn.q_proj"):
+            if cfg.q_lora_rank > 0:
+                q_lat_raw = L.wq_a(h, xq=hq)
+                if self.on_gpu:
+                    q_lat, q_lat_q = C.rms_norm(q_lat_raw, L.q_norm, cfg.rms_eps, want_bf16=True, want_fp8=True)
+                else:
+                    q_lat, q_lat_q = R.rms_norm(q_lat_raw, L.q_norm, cfg.rms_eps), None
+                q = L.wq_b(q_lat, xq=q_lat_q).view(T, Hl, dn + dr)
             else:
-                q_lat, q_lat_q = R.rms_norm(q_lat_raw, L.q_norm, cfg.rms_eps), None
-            q = L.wq_b(q_lat, xq=q_lat_q).view(T, Hl, dn + dr)
-        else:
-            q_lat = h
-            q = L.wq(h, xq=hq).view(T, Hl, dn + dr)
-        if not self.on_gpu:
-            q = q.clone()
-        C.rope_(q, dn, dr, self.cos_sin, fb.pos)
-        kv = L.wkv_a(h, xq=hq)                                                      # [T, r + dr]
-        kv_c = C.rms_norm(kv[:, :r].contiguous(), L.kv_norm, cfg.rms_eps) if self.on_gpu else \
-            R.rms_norm(kv[:, :r], L.kv_norm, cfg.rms_eps)
-        k_pe = kv[:, r:].contiguous().view(T, 1, dr)
-        C.rope_(k_pe, 0, dr, self.cos_sin, fb.pos)
-        latent = torch.cat([kv_c.to(self.act_dtype), k_pe.view(T, dr).to(self.act_dtype)], dim=-1)
-        cache.write_latent(i, fb.out_loc, latent)
+                q_lat = h
+                q = L.wq(h, xq=hq).view(T, Hl, dn + dr)
+            if not self.on_gpu:
+                q = q.clone()
+            C.rope_(q, dn, dr, self.cos_sin, fb.pos)
+        with region("attn.kv_proj"):
+            kv = L.wkv_a(h, xq=hq)                                                  # [T, r + dr]
+            kv_c = C.rms_norm(kv[:, :r].contiguous(), L.kv_norm, cfg.rms_eps) if self.on_gpu else \
+                R.rms_norm(kv[:, :r], L.kv_norm, cfg.rms_eps)
+            k_pe = kv[:, r:].contiguous().view(T, 1, dr)
+            C.rope_(k_pe, 0, dr, self.cos_sin, fb.pos)
+            latent = torch.cat([kv_c.to(self.act_dtype), k_pe.view(T, dr).to(self.act_dtype)], dim=-1)
+            cache.write_latent(i, fb.out_loc, latent)
         idx_state = None
         if cfg.use_indexer:
-            idx_state = self.indexer_qkw(i, h, q_lat, fb)
-            cache.write_index_k(i, fb.out_loc, idx_state[1])
+            with region("attn.indexer_qk"):
+                idx_state = self.indexer_qkw(i, h, q_lat, fb)
+                cache.write_index_k(i, fb.out_loc, idx_state[1])
         if fb.is_prefill:
             o = self._attn_prefill(i, q, kv_c, k_pe, fb, idx_state, cache)
         else:
             o = self._attn_decode(i, q, fb, cache, idx_state)
-        return L.wo(o.reshape(T, Hl * dv).to(self.act_dtype).contiguous())
+        with region("attn.o_proj"):
+            return L.wo(o.reshape(T, Hl * dv).to(self.act_dtype).contiguous())
 
     def indexer_qkw(self, i, h, q_lat, fb):
         cfg, L = self.cfg, self.layers[i]
@@ -307,47 +322,38 @@ class DeepseekModel:
         return q, k.view(T, Di), w
 
     def _prefill_key_masks(self, idx_state, fb: ForwardBatch):
-        cfg = self.cfg
         q, k, w = idx_state
-        masks = []
-        for b in range(len(fb.cu_seqlens) - 1):
-            s, t = fb.cu_seqlens[b], fb.cu_seqlens[b + 1]
-            n = t - s
-            if n <= cfg.index_topk:
-                masks.append(None)
-                continue
-            pos = torch.arange(n, device=q.device)
-            m = torch.zeros(n, n, dtype=torch.bool, device=q.device)
-            for c0 in range(0, n, 512):
-                c1 = min(n, c0 + 512)
-                lg = R.indexer_logits(q[s + c0:s + c1], k[s:t], w[s + c0:s + c1])
-                m[c0:c1] = R.topk_mask(lg, pos[c0:c1], pos, cfg.index_topk)
-            masks.append(m)
-        return masks if any(m is not None for m in masks) else None
+        return A.indexer_prefill_mask(q, k, w, fb.cu_seqlens, self.cfg.index_topk)
 
     def _attn_prefill(self, i, q, kv_c, k_pe, fb, idx_state, cache):
         cfg, L = self.cfg, self.layers[i]
         T, Hl = q.shape[0], self.H_local
         dn, dr, dv = cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.v_head_dim
-        kvb = L.wkv_b(kv_c.to(self.act_dtype)).view(T, Hl, dn + dv)
-        k = torch.cat([kvb[..., :dn], k_pe.to(kvb.dtype).expand(T, Hl, dr)], dim=-1)
-        v = kvb[..., dn:]
-        masks = self._prefill_key_masks(idx_state, fb) if idx_state is not None else None
-        return A.prefill_attention(q.contiguous(), k.contiguous(), v.contiguous(), fb.cu_seqlens,
-                                   cfg.softmax_scale, masks)
+        with region("attn.kv_up"):
+            kvb = L.wkv_b(kv_c.to(self.act_dtype)).view(T, Hl, dn + dv)
+            k = torch.cat([kvb[..., :dn], k_pe.to(kvb.dtype).expand(T, Hl, dr)], dim=-1)
+            v = kvb[..., dn:].contiguous()
+        with region("attn.indexer_topk"):
+            masks = self._prefill_key_masks(idx_state, fb) if idx_state is not None else None
+        with region("attn.core_prefill"):
+            return A.prefill_attention(q.contiguous(), k, v, fb.cu_seqlens, cfg.softmax_scale, masks)
 
     def _attn_decode(self, i, q, fb, cache, idx_state):
         cfg, L = self.cfg, self.layers[i]
         T, Hl = q.shape[0], self.H_local
         dn, r = cfg.qk_nope_head_dim, cfg.kv_lora_rank
-        q_abs = head_bmm(q[..., :dn], L.w_uk)                                        # [T, Hl, r]
-        qf = torch.cat([q_abs.to(self.act_dtype), q[..., dn:].to(self.act_dtype)], dim=-1).contiguous()
+        with region("attn.absorb_q"):
+            q_abs = head_bmm(q[..., :dn], L.w_uk)                                    # [T, Hl, r]
+            qf = torch.cat([q_abs.to(self.act_dtype), q[..., dn:].to(self.act_dtype)], dim=-1).contiguous()
         idx = fb.key_slots
         if idx_state is not None and int(fb.key_slots.shape[1]) > cfg.index_topk:
-            qi, _, wi = idx_state
-            idx = A.indexer_topk(qi, wi, cache.index_k[i], fb.key_slots, fb.n_keys, cfg.index_topk)
-        o_lat = A.sparse_mla(qf, cache.latent[i], idx.contiguous(), cfg.softmax_scale, r)   # [T, Hl, r]
-        return head_bmm(o_lat, L.w_uv)                                               # [T, Hl, dv]
+            with region("attn.indexer_topk"):
+                qi, _, wi = idx_state
+                idx = A.indexer_topk(qi, wi, cache.index_k[i], fb.key_slots, fb.n_keys, cfg.index_topk)
+        with region("attn.core_decode"):
+            o_lat = A.sparse_mla(qf, cache.latent[i], idx.contiguous(), cfg.softmax_scale, r)   # [T, Hl, r]
+        with region("attn.absorb_o"):
+            return head_bmm(o_lat, L.w_uv)                                           # [T, Hl, dv]
 
     # ------------------------------------------------------------------------------------------------------------------
     # FFN
@@ -355,12 +361,16 @@ class DeepseekModel:
     def ffn(self, i: int, h: torch.Tensor, hq) -> torch.Tensor:
         cfg, L = self.cfg, self.layers[i]
         if not L.moe:
-            return L.dense(h, xq=hq)
+            with region("ffn.dense"):
+                return L.dense(h, xq=hq)
         T = h.shape[0]
-        logits = bf16_gemm(h, L.gate_w, out_dtype=torch.float32) if self.on_gpu else h @ L.gate_w.t()
-        w, ids = C.router_topk(logits, L.gate_b, cfg.n_activated_experts, cfg.score_func, cfg.route_scale,
-                               cfg.norm_topk_prob)
-        shared = L.shared(h, xq=hq) if L.shared is not None else None
+        with region("moe.router"):
+            logits = L.gate(h, out_dtype=torch.float32)
+            w, ids = C.router_topk(logits, L.gate_b, cfg.n_activated_experts, cfg.score_func, cfg.route_scale,
+                                   cfg.norm_topk_prob)
+        self._tr(f"{i}.router_ids", ids)
+        with region("moe.shared"):
+            shared = L.shared(h, xq=hq) if L.shared is not None else None
         return self.pctx.moe(self, L, h, w, ids, shared)
 
     def moe_local(self, L, h, w, ids, shared):
@@ -377,13 +387,18 @@ class DeepseekModel:
                 y = R.swiglu(x @ L.e_w1[e].t(), x @ L.e_w3[e].t(), cfg.swiglu_limit) @ L.e_w2[e].t()
                 out.index_add_(0, rows, y * w[rows, slot][:, None])
             return out + shared if shared is not None else out
-        lay = C.MoeLayout(ids, self.E_local)
-        a_q, a_sf = quant_act(h, src_rows=lay.row_src)
+        with region("moe.dispatch"):
+            lay = C.MoeLayout(ids, self.E_local)
+            a_q, a_sf = quant_act(h, src_rows=lay.row_src)
         I2 = 2 * cfg.moe_intermediate
-        act, act_sf = fp8_gemm_swiglu(a_q, a_sf, L.e_w13, cfg.swiglu_limit, lay.m_block_expert, lay.num_blocks, I2)
-        y = fp8_gemm(act, act_sf, L.e_w2, m_block_expert=lay.m_block_expert, num_m_blocks=lay.num_blocks,
-                     n_per_group=cfg.hidden_size)
-        return C.moe_combine(y, w, lay.slot_pos, shared, T)
+        with region("moe.gemm_up"):
+            act, act_sf = fp8_gemm_swiglu(a_q, a_sf, L.e_w13, cfg.swiglu_limit, lay.m_block_expert, lay.num_blocks,
+                                          I2)
+        with region("moe.gemm_down"):
+            y = fp8_gemm(act, act_sf, L.e_w2, m_block_expert=lay.m_block_expert, num_m_blocks=lay.num_blocks,
+                         n_per_group=cfg.hidden_size)
+        with region("moe.combine"):
+            return C.moe_combine(y, w, lay.slot_pos, shared, T)
 
     # ------------------------------------------------------------------------------------------------------------------
     # whole model
@@ -398,18 +413,36 @@ class DeepseekModel:
 
     def forward(self, fb: ForwardBatch, cache) -> torch.Tensor:
         cfg = self.cfg
-        X, sumsq = self.embed_tokens(fb.ids)
+        with region("embed"):
+            X, sumsq = self.embed_tokens(fb.ids)
         for i in range(cfg.n_layers):
             L = self.layers[i]
-            pre, post, comb = self.hc_coeffs(X, sumsq, L.attn_hc)
-            h, hq = self.pre_norm(X, pre, L.attn_norm, want_fp8=self.on_gpu)
-            a = self.pctx.attn_out(self.attention(i, h, hq, fb, cache))
-            X, sumsq = self.post_mix(X, a, post, comb)
-            pre, post, comb = self.hc_coeffs(X, sumsq, L.ffn_hc)
-            h, hq = self.pre_norm(X, pre, L.ffn_norm, want_fp8=self.on_gpu)
+            with region("mhc.coeffs"):
+                pre, post, comb = self.hc_coeffs(X, sumsq, L.attn_hc)
+            with region("mhc.pre_norm"):
+                h, hq = self.pre_norm(X, pre, L.attn_norm, want_fp8=self.on_gpu)
+            a = self.attention(i, h, hq, fb, cache)
+            with region("tp.attn_out"):
+                a = self.pctx.attn_out(a)
+            self._tr(f"{i}.attn_in", h); self._tr(f"{i}.attn_pre", pre); self._tr(f"{i}.attn_out", a)
+            with region("mhc.post_mix"):
+                X, sumsq = self.post_mix(X, a, post, comb)
+            self._tr(f"{i}.X_attn", X)
+            with region("mhc.coeffs"):
+                pre, post, comb = self.hc_coeffs(X, sumsq, L.ffn_hc)
+            with region("mhc.pre_norm"):
+                h, hq = self.pre_norm(X, pre, L.ffn_norm, want_fp8=self.on_gpu)
             f = self.ffn(i, h, hq)
-            X, sumsq = self.post_mix(X, f, post, comb)
-        return self.logits(X, sumsq, fb.logits_rows)
+            self._tr(f"{i}.ffn_in", h); self._tr(f"{i}.ffn_out", f)
+            with region("mhc.post_mix"):
+                X, sumsq = self.post_mix(X, f, post, comb)
+            self._tr(f"{i}.X_ffn", X)
+        with region("head"):
+            return self.logits(X, sumsq, fb.logits_rows)
+
+    def _tr(self, name, t):
+        if self.trace is not None:
+            self.trace.append((name, t.detach().float().cpu().clone()))
 
     def logits(self, X, sumsq, rows: Optional[torch.Tensor]) -> torch.Tensor:
         cfg = self.cfg

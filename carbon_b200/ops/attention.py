@@ -29,14 +29,17 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seql
     out = torch.empty(T, H, dv, dtype=q.dtype if q.is_cuda else torch.float32, device=q.device)
     if q.is_cuda:
         e = ext()
-        if hasattr(e, "attn_prefill"):
-            cu = torch.tensor(cu_seqlens, dtype=torch.int32, device=q.device)
+        if hasattr(e, "attn_prefill") and q.shape[2] == 192 and v.shape[2] == 128:
             mask = None
-            if key_masks is not None and any(m is not None for m in key_masks):
+            if isinstance(key_masks, torch.Tensor):
+                mask = key_masks                              # already packed [T, W] bits
+            elif key_masks is not None and any(m is not None for m in key_masks):
                 mask = pack_key_mask(key_masks, cu_seqlens, q.device)
-            e.attn_prefill(q, k, v, cu, max(b - a for a, b in zip(cu_seqlens[:-1], cu_seqlens[1:])), float(scale),
-                           mask, out)
+            tiles = prefill_tiles(cu_seqlens).to(q.device, non_blocking=True)
+            e.attn_prefill(q, k, v, tiles, mask, float(scale), out, None)
             return out
+    if isinstance(key_masks, torch.Tensor):
+        key_masks = unpack_key_mask(key_masks, cu_seqlens)
     for b in range(len(cu_seqlens) - 1):
         s, t = cu_seqlens[b], cu_seqlens[b + 1]
         pos = torch.arange(t - s, device=q.device)
@@ -55,6 +58,16 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seql
     return out
 
 
+def prefill_tiles(cu_seqlens: List[int], bm: int = 128) -> torch.Tensor:
+    """(seq_start, seq_len, q0, 0) for every 128-query tile, longest causal work first (load balance)."""
+    tiles = []
+    for a, b in zip(cu_seqlens[:-1], cu_seqlens[1:]):
+        for q0 in range(0, b - a, bm):
+            tiles.append((a, b - a, q0, 0))
+    tiles.sort(key=lambda t: -t[2])
+    return torch.tensor(tiles, dtype=torch.int32).view(-1, 4)
+
+
 def pack_key_mask(key_masks, cu_seqlens, device) -> torch.Tensor:
     """Per-sequence bool masks -> one uint32 bit matrix [T, ceil(Lmax/32)] (bit j of word w = key 32w+j)."""
     T = cu_seqlens[-1]
@@ -71,6 +84,41 @@ def pack_key_mask(key_masks, cu_seqlens, device) -> torch.Tensor:
     shifts = torch.arange(32, device=device, dtype=torch.int64)
     words = (w << shifts).sum(-1)
     return words.to(torch.int64).bitwise_and(0xFFFFFFFF).to(torch.int32).contiguous()
+
+
+def unpack_key_mask(words: torch.Tensor, cu_seqlens: List[int]) -> List[torch.Tensor]:
+    shifts = torch.arange(32, device=words.device, dtype=torch.int64)
+    bits = ((words.to(torch.int64)[..., None] >> shifts) & 1).bool().reshape(words.shape[0], -1)
+    return [bits[a:b, : b - a] for a, b in zip(cu_seqlens[:-1], cu_seqlens[1:])]
+
+
+def indexer_prefill_mask(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, cu_seqlens: List[int],
+                         topk: int) -> Optional[torch.Tensor]:
+    """DSA selection for a prefill batch: per sequence, logits of every (query, causal key) pair and exact top-k.
+    q [T, Hi, Di], k [T, Di], w [T, Hi]. Returns packed bits [T, ceil(Lmax/32)] (None when no sequence exceeds
+    top-k, i.e. attention stays dense causal)."""
+    lens = [b - a for a, b in zip(cu_seqlens[:-1], cu_seqlens[1:])]
+    if max(lens) <= topk:
+        return None
+    T, W = cu_seqlens[-1], (max(lens) + 31) // 32
+    if q.is_cuda:
+        e = ext()
+        mask = torch.empty(T, W, dtype=torch.int32, device=q.device)
+        for a, b in zip(cu_seqlens[:-1], cu_seqlens[1:]):
+            n = b - a
+            ldo = (n + 3) // 4 * 4
+            logits = torch.empty(n, ldo, dtype=torch.float32, device=q.device)
+            if n > topk:
+                e.indexer_logits(k[a:b].contiguous(), q[a:b].contiguous(), w[a:b].float().contiguous(), logits, True)
+            e.topk_mask(logits, n, topk, mask, a)
+        return mask
+    masks = []
+    for a, b in zip(cu_seqlens[:-1], cu_seqlens[1:]):
+        n = b - a
+        pos = torch.arange(n)
+        lg = R.indexer_logits(q[a:b], k[a:b], w[a:b])
+        masks.append(R.topk_mask(lg, pos, pos, topk))
+    return pack_key_mask(masks, cu_seqlens, q.device)
 
 
 def sparse_mla(q: torch.Tensor, kv: torch.Tensor, idx: torch.Tensor, scale: float, d_latent: int) -> torch.Tensor:

@@ -107,6 +107,7 @@ class RefModel:
     def __init__(self, cfg: ModelConfig, weights: Dict[str, torch.Tensor]):
         self.cfg = cfg
         self.w = {k: v.float() for k, v in weights.items()}
+        self.forced_routing = None   # {layer: ids [T, k]}: use these expert choices instead of the router's top-k
 
     # -- sublayers -------------------------------------------------------------------------------------------------
     def attention(self, i: int, h: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
@@ -157,6 +158,14 @@ class RefModel:
         logits = h @ w[L + "gate.weight"].t()
         wts, ids = ops.router_topk(logits, w[L + "gate.bias"], cfg.n_activated_experts, cfg.score_func,
                                    cfg.route_scale, cfg.norm_topk_prob)
+        if self.forced_routing is not None and i in self.forced_routing:
+            ids = self.forced_routing[i].to(ids.dtype)
+            act = torch.sigmoid(logits) if cfg.score_func == "sigmoid" else (
+                torch.sqrt(ops.softplus(logits)) if cfg.score_func == "sqrtsoftplus" else torch.softmax(logits, -1))
+            wts = act.gather(1, ids.long())
+            if cfg.norm_topk_prob:
+                wts = wts / (wts.sum(-1, keepdim=True) + 1e-20)
+            wts = wts * cfg.route_scale
         out = torch.zeros_like(h)
         for e in range(cfg.n_routed_experts):
             rows, slot = torch.nonzero(ids == e, as_tuple=True)

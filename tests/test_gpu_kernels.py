@@ -275,3 +275,65 @@ def test_mhc_kernels():
     Xn_ref = R.mhc_post_mix(X.float(), out.float(), post_r, comb_r)
     assert rel_err(Xn, Xn_ref) < 5e-3
     assert rel_err(ss2, Xn.float().pow(2).sum((1, 2))) < 1e-4
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# attention
+# ----------------------------------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("lens,masked", [([128], False), ([300, 77, 5], False), ([513], True), ([200, 260], True)])
+def test_attn_prefill(lens, masked):
+    from carbon_b200.ops.attention import prefill_attention
+
+    torch.manual_seed(5)
+    H = 4
+    T = sum(lens)
+    q = torch.randn(T, H, 192).to(torch.bfloat16)
+    k = torch.randn(T, H, 192).to(torch.bfloat16)
+    v = torch.randn(T, H, 128).to(torch.bfloat16)
+    cu = [0]
+    for n in lens:
+        cu.append(cu[-1] + n)
+    masks = None
+    if masked:
+        masks = [torch.rand(n, n) < 0.3 for n in lens]
+        for m in masks:
+            m.fill_diagonal_(True)
+    out = prefill_attention(q.to(DEV), k.to(DEV), v.to(DEV), cu, 192 ** -0.5,
+                            [m.to(DEV) for m in masks] if masks else None)
+    torch.cuda.synchronize()
+    for b in range(len(lens)):
+        s, t = cu[b], cu[b + 1]
+        pos = torch.arange(t - s)
+        ref = R.causal_attention(q[s:t], k[s:t], v[s:t], 192 ** -0.5, pos, pos, masks[b] if masks else None)
+        assert rel_err(out[s:t], ref) < 1e-2, (b, rel_err(out[s:t], ref))
+
+
+@pytest.mark.parametrize("n,H", [(300, 64), (700, 32)])
+def test_indexer_logits_gemm(n, H):
+    torch.manual_seed(6)
+    q = torch.randn(n, H, 128).to(torch.bfloat16)
+    k = torch.randn(n, 128).to(torch.bfloat16)
+    w = torch.randn(n, H)
+    ldo = (n + 3) // 4 * 4
+    out = torch.full((n, ldo), float("nan"), device=DEV)
+    _ext().indexer_logits(k.to(DEV), q.to(DEV), w.to(DEV), out, True)
+    ref = R.indexer_logits(q.float(), k.float(), w)
+    causal = torch.ones(n, n, dtype=torch.bool).tril_()
+    got = out[:, :n].cpu()
+    assert rel_err(got[causal], ref[causal]) < 1e-5
+
+
+@pytest.mark.parametrize("n,k", [(100, 128), (300, 64), (1000, 256), (2000, 512)])
+def test_topk_mask_exact(n, k):
+    from carbon_b200.ops.attention import unpack_key_mask
+
+    torch.manual_seed(7)
+    logits = torch.randn(n, n)
+    logits[:, ::7] = 0.5            # ties, resolved toward the lower key index
+    W = (n + 31) // 32
+    mask = torch.zeros(n, W, dtype=torch.int32, device=DEV)
+    _ext().topk_mask(logits.to(DEV), n, k, mask, 0)
+    got = unpack_key_mask(mask.cpu(), [0, n])[0]
+    pos = torch.arange(n)
+    exp = R.topk_mask(logits, pos, pos, k)
+    assert torch.equal(got, exp)
