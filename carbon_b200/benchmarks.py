@@ -1,0 +1,181 @@
+"""Op-level benchmarks for the BASELINE configs, timed on the device with CUDA events and reported against the
+measured roofline (``MEASURED_PEAKS.json`` when present: ``bf16_tflops``, ``hbm_gbs``).
+
+    python -m carbon_b200.benchmarks attn  [--batch 4 --seq 8192 --heads 128 --dsa]   # config 2
+    python -m carbon_b200.benchmarks mhc   [--tokens 16384 --hidden 7168 --n 24576]   # config 3
+    python -m carbon_b200.benchmarks gemm  [--m 16384 --n 24576 --k 7168]             # fp8 block-scaled GEMM
+    python -m carbon_b200.benchmarks moe   [--tokens 4096 --experts 256 --topk 8]     # config 4, one GPU
+    python -m carbon_b200.benchmarks decode_attn [--batch 32 --topk 2048]
+
+Each prints one JSON line.  Inputs are larger than L2 where the config allows; between timed iterations a 256 MB
+buffer is rewritten to flush L2 (``flush_l2``) for the ones that are not.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import sys
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"bf16_tflops": d.get("bf16_tflops", 1590.0), "hbm_gbs": d.get("hbm_gbs", 6650.0), "src": "measured"}
+    return {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0, "src": "fallback"}
+
+
+_FLUSH = None
+
+
+def flush_l2():
+    global _FLUSH
+    if _FLUSH is None:
+        _FLUSH = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    _FLUSH.fill_(1)
+
+
+def time_fn(fn, iters=10, warmup=3, flush=True):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    ts = []
+    for _ in range(iters):
+        if flush:
+            flush_l2()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        ts.append(a.elapsed_time(b))
+    ts.sort()
+    return ts[len(ts) // 2]
+
+
+def bench_attn(a):
+    from .ops.attention import indexer_prefill_mask, mla_prefill
+
+    torch.manual_seed(0)
+    B, S, H = a.batch, a.seq, a.heads
+    T = B * S
+    q = torch.randn(T, H, 192, device="cuda", dtype=torch.bfloat16)
+    kvb = torch.randn(T, H, 256, device="cuda", dtype=torch.bfloat16)   # (k_nope | v) as the wkv_b GEMM writes it
+    kpe = torch.randn(T, 64, device="cuda", dtype=torch.bfloat16)       # shared RoPE key
+    cu = [i * S for i in range(B + 1)]
+    mask = None
+    res = {}
+    if a.dsa:
+        qi = torch.randn(T, 64, 128, device="cuda").to(torch.float8_e4m3fn).to(torch.bfloat16)
+        ki = torch.randn(T, 128, device="cuda").to(torch.float8_e4m3fn).to(torch.bfloat16)
+        wi = torch.randn(T, 64, device="cuda") * (64 ** -0.5) * (128 ** -0.5)
+        ms = time_fn(lambda: indexer_prefill_mask(qi, ki, wi, cu, a.topk), iters=5)
+        mask = indexer_prefill_mask(qi, ki, wi, cu, a.topk)
+        idx_flops = B * (S * S / 2) * 64 * 128 * 2
+        res["indexer_ms"] = round(ms, 3)
+        res["indexer_tflops"] = round(idx_flops / ms / 1e9, 1)
+    ms = time_fn(lambda: mla_prefill(q, kvb, kpe, cu, 192 ** -0.5, mask), iters=5)
+    flops = B * H * (S * S / 2) * (192 + 128) * 2
+    pk = peaks()
+    res.update({"bench": "mla_prefill_attention", "batch": B, "seq": S, "heads": H, "dsa": a.dsa, "ms": round(ms, 3),
+                "tflops": round(flops / ms / 1e9, 1),
+                "frac_of_bf16_peak": round(flops / ms / 1e9 / pk["bf16_tflops"], 3), "peak_src": pk["src"],
+                "flops_counted": "dense causal (masked DSA keys still cost a full tile)"})
+    print(json.dumps(res))
+
+
+def bench_gemm(a):
+    from .ops.gemm import fp8_gemm
+    from .ops.quant import quant_act, quantize_weight
+
+    x = torch.randn(a.m, a.k, device="cuda").to(torch.bfloat16)
+    W = quantize_weight(torch.randn(a.n, a.k, device="cuda") * 0.02)
+    q, sf = quant_act(x)
+    out = torch.empty(a.m, a.n, dtype=torch.bfloat16, device="cuda")
+    ms = time_fn(lambda: fp8_gemm(q, sf, W, out=out))
+    flops = 2 * a.m * a.n * a.k
+    pk = peaks()
+    print(json.dumps({"bench": "fp8_gemm", "m": a.m, "n": a.n, "k": a.k, "ms": round(ms, 3),
+                      "tflops": round(flops / ms / 1e9, 1),
+                      "frac_of_bf16_peak_x2": round(flops / ms / 1e9 / (2 * pk["bf16_tflops"]), 3),
+                      "peak_src": pk["src"]}))
+
+
+def bench_mhc(a):
+    """Config 3: mHC stream mix (Sinkhorn-projected comb) + RMSNorm + fp8 quant feeding a 7168->24576 fp8 GEMM."""
+    from .ops._ext import ext
+    from .ops.gemm import fp8_gemm
+    from .ops.quant import empty_sf, quantize_weight
+    from .ref import ops as R
+
+    T, D, N = a.tokens, a.hidden, a.n
+    X = torch.randn(T, 4, D, device="cuda").to(torch.bfloat16)
+    g = torch.Generator().manual_seed(0)
+    comb = R.sinkhorn(torch.randn(4, 4, generator=g), 20, 1e-6)
+    pre = comb.sum(0) / 4                              # stream weights of the mixed read (column means)
+    pre_t = pre.to("cuda").expand(T, 4).contiguous()
+    w_norm = torch.ones(D, device="cuda")
+    W = quantize_weight(torch.randn(N, D, device="cuda") * 0.02)
+    y = torch.empty(T, D, dtype=torch.bfloat16, device="cuda")
+    q = torch.empty(T, D, dtype=torch.float8_e4m3fn, device="cuda")
+    sf = empty_sf(T, D, "cuda")
+    out = torch.empty(T, N, dtype=torch.bfloat16, device="cuda")
+
+    def step():
+        ext().mhc_pre_norm(X, pre_t, w_norm, 1e-6, None, q, sf, None)
+        fp8_gemm(q, sf, W, out=out)
+
+    ms = time_fn(step, flush=False)
+    ms_mix = time_fn(lambda: ext().mhc_pre_norm(X, pre_t, w_norm, 1e-6, None, q, sf, None), flush=False)
+    flops = 2 * T * N * D
+    bytes_mix = T * 4 * D * 2 + T * D
+    pk = peaks()
+    print(json.dumps({"bench": "mhc_mix_norm_fp8_gemm", "tokens": T, "hidden": D, "n": N, "ms": round(ms, 3),
+                      "mix_norm_quant_ms": round(ms_mix, 3),
+                      "mix_gbs": round(bytes_mix / ms_mix / 1e6, 1),
+                      "mix_frac_of_hbm": round(bytes_mix / ms_mix / 1e6 / pk["hbm_gbs"], 3),
+                      "gemm_tflops": round(flops / (ms - ms_mix) / 1e9, 1), "peak_src": pk["src"]}))
+
+
+def bench_decode_attn(a):
+    from .ops.attention import sparse_mla
+
+    T, H, K, S = a.batch, a.heads, a.topk, a.batch * a.context
+    q = torch.randn(T, H, 576, device="cuda").to(torch.bfloat16)
+    kv = torch.randn(S, 576, device="cuda").to(torch.bfloat16)
+    idx = torch.stack([torch.randperm(a.context, device="cuda")[:K] + b * a.context for b in range(T)]).int()
+    ms = time_fn(lambda: sparse_mla(q, kv, idx, 192 ** -0.5, 512))
+    bytes_kv = T * K * 576 * 2
+    pk = peaks()
+    print(json.dumps({"bench": "sparse_mla_decode", "batch": T, "heads": H, "topk": K, "ms": round(ms, 4),
+                      "kv_gbs": round(bytes_kv / ms / 1e6, 1),
+                      "frac_of_hbm": round(bytes_kv / ms / 1e6 / pk["hbm_gbs"], 3),
+                      "tflops": round(T * H * K * (576 + 512) * 2 / ms / 1e9, 1), "peak_src": pk["src"]}))
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("what", choices=["attn", "gemm", "mhc", "decode_attn"])
+    ap.add_argument("--batch", type=int, default=4)
+    ap.add_argument("--seq", type=int, default=8192)
+    ap.add_argument("--heads", type=int, default=128)
+    ap.add_argument("--dsa", action="store_true")
+    ap.add_argument("--topk", type=int, default=2048)
+    ap.add_argument("--context", type=int, default=4096)
+    ap.add_argument("--m", type=int, default=16384)
+    ap.add_argument("--n", type=int, default=24576)
+    ap.add_argument("--k", type=int, default=7168)
+    ap.add_argument("--tokens", type=int, default=16384)
+    ap.add_argument("--hidden", type=int, default=7168)
+    a = ap.parse_args(argv)
+    sys.path.insert(0, ROOT)
+    {"attn": bench_attn, "gemm": bench_gemm, "mhc": bench_mhc, "decode_attn": bench_decode_attn}[a.what](a)
+
+
+if __name__ == "__main__":
+    main()

@@ -132,7 +132,7 @@ def small_gpu_config() -> ModelConfig:
     return ModelConfig(
         vocab_size=8192, hidden_size=1024, n_layers=4, n_dense_layers=1, dense_intermediate=2048,
         n_heads=16, q_lora_rank=512, kv_lora_rank=512, qk_nope_head_dim=128, qk_rope_head_dim=64, v_head_dim=128,
-        max_position=8192, index_n_heads=8, index_head_dim=128, index_topk=256,
+        max_position=8192, index_n_heads=16, index_head_dim=128, index_topk=256,
         n_routed_experts=32, n_activated_experts=4, n_shared_experts=1, moe_intermediate=256,
         route_scale=2.5,
     )

@@ -1,0 +1,372 @@
+// Absorbed-MLA sparse attention (decode / long-context) on tcgen05 (sm_100a).
+//
+//   o_lat[t, h, :] = softmax_j( q[t, h, :] · kv[idx[t, j], :] · scale ) · kv[idx[t, j], :512]
+//
+// q: [T, H, 576] bf16 (512 absorbed-nope + 64 rope), kv: latent cache [S, 576] bf16, idx: [T, K] int32 cache slots
+// (-1 = no key).  All H <= 128 heads of a token share every KV row (MQA), so a CTA computes S[128 heads, 16 keys]
+// = Q·Kᵀ with M = 128 (heads) and streams the token's selected rows through shared memory with TMA gather4 (four
+// 128-byte row pieces per instruction, one-row-high box).  The value half (256 of the 512 latent dims) of the CTA
+// accumulates O[128, 256] in TMEM; the other half is computed by a sibling CTA (both need all of S).  Keys are split
+// across CTAs (flash-decoding); a combine kernel merges the (m, l, O) partials.
+//
+// Roles (256 threads): warp 0 TMA (Q once, then gathered KV tiles, 3-stage ring), warp 1 MMA, warp 2 TMEM,
+// warps 4-7 softmax (one head row per thread, lazy O rescale).  Every wait is bounded.
+// Reference kernels with the same role: FlashMLA-derived decode / verify attention over the paged latent cache
+// (king_v10/bundle_v9/dec/cuda_decode_attn.py:20-116, dec/cuda_vattn.py:4654).
+#include <cudaTypedefs.h>
+#include "ptx.cuh"
+
+namespace cb {
+namespace mla {
+
+constexpr int HM = 128;                // head rows per CTA (M)
+constexpr int D = 576, DL = 512, DHALF = 256;
+constexpr int KT = 16;                 // keys per tile (N of Q·Kᵀ, K of P·V)
+constexpr int STAGES = 3;
+constexpr int Q_ATOM = HM * 128;       // 16 KB: 128 rows x 64 dims
+constexpr int KV_ATOM = KT * 128;      // 2 KB: 16 rows x 64 dims
+constexpr int Q_BYTES = 9 * Q_ATOM;    // 144 KB
+constexpr int KV_BYTES = 9 * KV_ATOM;  // 18 KB per stage
+constexpr int P_BYTES = HM * 128;      // 16 KB (16 keys used of a 64-key swizzle atom)
+constexpr int SMEM = 1024 + Q_BYTES + STAGES * KV_BYTES + P_BYTES + 256;
+constexpr float kRescaleThresh = 8.0f;
+
+struct Params {
+  const int* idx;          // [T, K]
+  int K;                   // keys per token in idx
+  int H;
+  int n_splits, chunk;     // keys [split*chunk, (split+1)*chunk) of each token's list
+  float scale_log2;
+  float* part_o;           // [T, n_splits, H, 512] fp32 (n_splits > 1)
+  float* part_ml;          // [T, n_splits, H, 2]  (m in log2 units, l)
+  __nv_bfloat16* out;      // [T, H, 512] when n_splits == 1
+  int* status;
+};
+
+CB_DEVICE uint64_t desc_mn_sw128(const void* p, uint32_t lbo, uint32_t sbo) {
+  const uint64_t addr = smem_u32(p);
+  return ((addr >> 4) & 0x3FFFull) | (uint64_t((lbo >> 4) & 0x3FFF) << 16) | (uint64_t((sbo >> 4) & 0x3FFF) << 32) |
+         (uint64_t(1) << 46) | (uint64_t(2) << 61);
+}
+
+CB_DEVICE void tma_gather4(void* dst, const void* tmap, uint64_t* bar, int col, int r0, int r1, int r2, int r3) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];"
+      ::"r"(smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(tmap)), "r"(smem_u32(bar)), "r"(col), "r"(r0), "r"(r1),
+      "r"(r2), "r"(r3)
+      : "memory");
+}
+
+__global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constant__ CUtensorMap tm_q,
+                                                            const __grid_constant__ CUtensorMap tm_kv,
+                                                            const Params p) {
+#if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 1000
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sKV = sQ + Q_BYTES;
+  uint8_t* sP = sKV + STAGES * KV_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + P_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;              // [STAGES]
+  uint64_t* kv_empty = bars + 1 + STAGES;    // [STAGES]
+  uint64_t* s_full = bars + 1 + 2 * STAGES;  // [2]
+  uint64_t* s_empty = s_full + 2;            // [2]
+  uint64_t* p_full = s_empty + 2;
+  uint64_t* pv_done = p_full + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int t = blockIdx.x, hh = blockIdx.y, split = blockIdx.z;
+  const int k_begin = split * p.chunk;
+  const int k_end = min(p.K, k_begin + p.chunk);
+  const int n_tiles = k_end > k_begin ? (k_end - k_begin + KT - 1) / KT : 0;
+  const int* idx_t = p.idx + size_t(t) * p.K;
+  const uint32_t warp = warp_id(), lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < STAGES; ++i) { mbar_init(&kv_full[i], 1); mbar_init(&kv_empty[i], 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_empty[i], 128); }
+    mbar_init(p_full, 128); mbar_init(pv_done, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto fail = [&](int code) { if (p.status) atomicCAS(p.status, 0, code); *abort_flag = 1; };
+
+  if (warp == 0) {
+    // ---------------- TMA: Q once, then gathered KV rows ----------------
+    if (lane == 0 && n_tiles > 0) {
+      tma_prefetch_desc(&tm_q); tma_prefetch_desc(&tm_kv);
+      mbar_arrive_expect_tx(q_full, Q_BYTES);
+      for (int a = 0; a < 9; ++a) tma_load_3d(sQ + a * Q_ATOM, &tm_q, q_full, a * 64, 0, t);
+    }
+    for (int j = 0; j < n_tiles; ++j) {
+      const int s = j % STAGES;
+      const int key = k_begin + j * KT + lane;
+      int slot = (lane < KT && key < k_end) ? idx_t[key] : 0;
+      if (slot < 0) slot = 0;                                  // masked in softmax; keep the address valid
+      int ok = 1;
+      if (lane == 0) {
+        ok = mbar_wait(&kv_empty[s], ((j / STAGES) & 1) ^ 1) ? 1 : 0;
+        if (ok) mbar_arrive_expect_tx(&kv_full[s], KV_BYTES);
+        else fail(kErrTimeoutEmpty);
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok || *abort_flag) break;
+      int r[KT];
+#pragma unroll
+      for (int i = 0; i < KT; ++i) r[i] = __shfl_sync(0xffffffffu, slot, i);
+      if (lane < 9) {                                          // lane a issues the 4 gathers of 64-dim atom a
+        uint8_t* dst = sKV + s * KV_BYTES + lane * KV_ATOM;
+#pragma unroll
+        for (int g = 0; g < 4; ++g)
+          tma_gather4(dst + g * 4 * 128, &tm_kv, &kv_full[s], lane * 64, r[4 * g], r[4 * g + 1], r[4 * g + 2],
+                      r[4 * g + 3]);
+      }
+      __syncwarp();
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA ----------------
+    if (elect_one()) {
+      const uint32_t id_qk = idesc_bf16(HM, KT);
+      const uint32_t id_pv = idesc_bf16(HM, DHALF) | (1u << 16);   // B (V) MN-major
+      bool ok = n_tiles == 0 || mbar_wait(q_full, 0);
+      if (!ok) fail(kErrTimeoutFull);
+      auto issue_qk = [&](int j) -> bool {
+        const int s = j % STAGES, b = j & 1;
+        if (!mbar_wait(&kv_full[s], (j / STAGES) & 1)) { fail(kErrTimeoutFull); return false; }
+        if (!mbar_wait(&s_empty[b], ((j >> 1) & 1) ^ 1)) { fail(kErrTimeoutTmem); return false; }
+        tc_fence_after();
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int a = kk >> 2, off = (kk & 3) * 32;
+          mma_f16_ss(tmem + b * 32, smem_desc_sw128(sQ + a * Q_ATOM + off),
+                     smem_desc_sw128(sKV + s * KV_BYTES + a * KV_ATOM + off), id_qk, kk > 0);
+        }
+        mma_commit(&s_full[b]);
+        return true;
+      };
+      auto issue_pv = [&](int j) -> bool {
+        const int s = j % STAGES;
+        if (!mbar_wait(p_full, j & 1)) { fail(kErrTimeoutFull); return false; }
+        tc_fence_after();
+        mma_f16_ss(tmem + 256, smem_desc_sw128(sP),
+                   desc_mn_sw128(sKV + s * KV_BYTES + (hh * 4) * KV_ATOM, KV_ATOM, 1024), id_pv, j > 0);
+        mma_commit(pv_done);
+        mma_commit(&kv_empty[s]);
+        return true;
+      };
+      if (ok && n_tiles > 0) ok = issue_qk(0);
+      for (int j = 0; ok && j < n_tiles && !*abort_flag; ++j) {
+        if (j + 1 < n_tiles) ok = issue_qk(j + 1);
+        if (ok) ok = issue_pv(j);
+      }
+    }
+  } else if (warp >= 4) {
+    // ---------------- softmax / rescale / epilogue ----------------
+    const uint32_t q = warp & 3;
+    const int row = q * 32 + lane;               // head
+    const uint32_t t_lane = tmem + ((q * 32) << 16);
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int b = j & 1;
+      if (!mbar_wait(&s_full[b], (j >> 1) & 1)) { fail(kErrTimeoutTmem); ok = false; break; }
+      tc_fence_after();
+      uint32_t r[16];
+      tmem_ld_32x32b_x16(t_lane + b * 32, r);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&s_empty[b]);
+      float sv[KT];
+      float mt = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < KT; ++i) {
+        const int key = k_begin + j * KT + i;
+        const bool valid = key < k_end && __ldg(idx_t + key) >= 0;
+        sv[i] = valid ? __uint_as_float(r[i]) * p.scale_log2 : -INFINITY;
+        mt = fmaxf(mt, sv[i]);
+      }
+      const bool need = (j > 0) && (mt > m_used + kRescaleThresh);
+      const float m_new = (need || j == 0) ? fmaxf(m_used, mt) : m_used;
+      const float m_ref = m_new == -INFINITY ? 0.f : m_new;
+      float alpha = 1.f;
+      if (need && m_used != -INFINITY) alpha = exp2f(m_used - m_ref);
+      float rs = 0.f;
+      uint32_t pk[KT / 2];
+#pragma unroll
+      for (int i = 0; i < KT; i += 2) {
+        const float a0 = exp2f(sv[i] - m_ref), a1 = exp2f(sv[i + 1] - m_ref);
+        rs += a0 + a1;
+        pk[i / 2] = pack_bf16x2(a0, a1);
+      }
+      l = l * alpha + rs;
+      m_used = m_new;
+      if (j > 0) {
+        if (!mbar_wait(pv_done, (j - 1) & 1)) { fail(kErrTimeoutTmem); ok = false; break; }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, need)) {
+#pragma unroll 1
+          for (int c = 0; c < DHALF; c += 16) {
+            uint32_t o[16];
+            tmem_ld_32x32b_x16(t_lane + 256 + c, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st_32x32b_x16(t_lane + 256 + c, o);
+          }
+          tmem_st_wait();
+        }
+      }
+      // P row: 16 keys = the first two 16-byte chunks of a 128-byte swizzled row
+      uint8_t* prow = sP + row * 128;
+      *reinterpret_cast<uint4*>(prow + ((0 ^ (row & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      *reinterpret_cast<uint4*>(prow + ((1 ^ (row & 7)) << 4)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      fence_proxy_async();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    if (ok && n_tiles > 0) {
+      if (!mbar_wait(pv_done, (n_tiles - 1) & 1)) { fail(kErrTimeoutTmem); ok = false; }
+      tc_fence_after();
+    }
+    const bool head_ok = row < p.H;
+    if (p.n_splits > 1) {
+      if (ok && head_ok && hh == 0) {
+        float* ml = p.part_ml + ((size_t(t) * p.n_splits + split) * p.H + row) * 2;
+        ml[0] = m_used == -INFINITY ? -INFINITY : m_used;
+        ml[1] = l;
+      }
+    }
+    if (ok) {
+      const float inv = (p.n_splits == 1 && l > 0.f) ? 1.f / l : 1.f;
+#pragma unroll 1
+      for (int c = 0; c < DHALF; c += 32) {
+        uint32_t v[32];
+        if (n_tiles > 0) {
+          tmem_ld_32x32b_x32(t_lane + 256 + c, v);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0u;
+        }
+        if (!head_ok) continue;
+        if (p.n_splits == 1) {
+          __nv_bfloat16* o = p.out + (size_t(t) * p.H + row) * DL + hh * DHALF + c;
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            uint4 u;
+            u.x = pack_bf16x2(__uint_as_float(v[8 * w + 0]) * inv, __uint_as_float(v[8 * w + 1]) * inv);
+            u.y = pack_bf16x2(__uint_as_float(v[8 * w + 2]) * inv, __uint_as_float(v[8 * w + 3]) * inv);
+            u.z = pack_bf16x2(__uint_as_float(v[8 * w + 4]) * inv, __uint_as_float(v[8 * w + 5]) * inv);
+            u.w = pack_bf16x2(__uint_as_float(v[8 * w + 6]) * inv, __uint_as_float(v[8 * w + 7]) * inv);
+            reinterpret_cast<uint4*>(o)[w] = u;
+          }
+        } else {
+          float* o = p.part_o + ((size_t(t) * p.n_splits + split) * p.H + row) * DL + hh * DHALF + c;
+#pragma unroll
+          for (int w = 0; w < 8; ++w)
+            reinterpret_cast<uint4*>(o)[w] = make_uint4(v[4 * w], v[4 * w + 1], v[4 * w + 2], v[4 * w + 3]);
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 2) { tc_fence_after(); tmem_dealloc(tmem, 512); }
+#endif
+}
+
+// out[t, h, :] = Σ_s 2^(m_s - M) O_s / Σ_s 2^(m_s - M) l_s
+__global__ void mla_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int n_splits,
+                                   int H, __nv_bfloat16* __restrict__ out) {
+  const int t = blockIdx.x, h = blockIdx.y;
+  float M = -INFINITY;
+  for (int s = 0; s < n_splits; ++s) M = fmaxf(M, part_ml[((size_t(t) * n_splits + s) * H + h) * 2]);
+  float L = 0.f;
+  for (int s = 0; s < n_splits; ++s) {
+    const float* ml = part_ml + ((size_t(t) * n_splits + s) * H + h) * 2;
+    if (ml[0] != -INFINITY) L += exp2f(ml[0] - M) * ml[1];
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  for (int c = threadIdx.x; c < DL; c += blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < n_splits; ++s) {
+      const float m = part_ml[((size_t(t) * n_splits + s) * H + h) * 2];
+      if (m == -INFINITY) continue;
+      acc += exp2f(m - M) * part_o[((size_t(t) * n_splits + s) * H + h) * DL + c];
+    }
+    out[(size_t(t) * H + h) * DL + c] = __float2bfloat16_rn(acc * inv);
+  }
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess && q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+}  // namespace mla
+
+// q [T,H,576], kv [S,576] bf16; idx [T,K]; out [T,H,512] bf16. part_o/part_ml: workspace for n_splits > 1
+// (sizes T*n_splits*H*512 and T*n_splits*H*2 floats).
+cudaError_t sparse_mla(const void* q, int T, int H, const void* kv, int S, const int* idx, int K, float scale,
+                       int n_splits, float* part_o, float* part_ml, void* out, int* status, cudaStream_t s) {
+  using namespace mla;
+  if (T == 0) return cudaSuccess;
+  if (H > HM || n_splits < 1) return cudaErrorInvalidValue;
+  auto fn = encode_fn();
+  if (!fn) return cudaErrorInvalidValue;
+  CUtensorMap tq, tkv;
+  {
+    cuuint64_t dims[3] = {D, cuuint64_t(H), cuuint64_t(T)};
+    cuuint64_t str[2] = {D * 2, cuuint64_t(H) * D * 2};
+    cuuint32_t box[3] = {64, HM, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    if (fn(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, str, box, es,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  {
+    cuuint64_t dims[2] = {D, cuuint64_t(S)};
+    cuuint64_t str[1] = {D * 2};
+    cuuint32_t box[2] = {64, 1};
+    cuuint32_t es[2] = {1, 1};
+    if (fn(&tkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(kv), dims, str, box, es,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+  }
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(sparse_mla_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  Params p;
+  p.idx = idx; p.K = K; p.H = H; p.n_splits = n_splits;
+  p.chunk = ((K + n_splits - 1) / n_splits + KT - 1) / KT * KT;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.part_o = part_o; p.part_ml = part_ml;
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.status = status;
+  sparse_mla_kernel<<<dim3(T, 2, n_splits), 256, SMEM, s>>>(tq, tkv, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || n_splits == 1) return e;
+  mla_combine_kernel<<<dim3(T, H), 128, 0, s>>>(part_o, part_ml, n_splits, H, reinterpret_cast<__nv_bfloat16*>(out));
+  return cudaGetLastError();
+}
+
+}  // namespace cb

@@ -4,9 +4,10 @@
 // CTA roles (256 threads):
 //   warp 0  TMA: Q once, then K tiles into a 2-deep ring          warp 3  TMA: V tiles (1 stage)
 //   warp 1  MMA: S[j%2] = Q·K_jᵀ (TMEM), O += P_j·V_j (TMEM)        warp 2  TMEM allocator
-//   warps 4-7 softmax: one query row per thread; S from TMEM, P (bf16) to shared memory in the 128B-swizzled
-//            K-major layout the MMA reads, lazy rescale of O in TMEM (only when the row max grows by > 2^8),
-//            final O/l to global.
+//   warps 4-11 softmax: two warps per TMEM lane quadrant, each one query row x 64 score columns per thread;
+//            row max exchanged through shared memory; P (bf16) to shared memory in the 128B-swizzled K-major
+//            layout the MMA reads; lazy rescale of O in TMEM (only when the row max grows by > 2^8); O/l out.
+//            Tiles wholly below the diagonal and without a DSA mask skip the per-key mask work.
 // TMEM: S0 cols [0,128), S1 [128,256), O [256,384).
 // Shared memory: Q 48 KB | K 2 x 48 KB | V 32 KB | P 32 KB  (= 208 KB) + barriers.
 //
@@ -31,7 +32,7 @@ constexpr int K_BYTES = BN * DQK * 2;          // 48 KB
 constexpr int V_BYTES = BN * DV * 2;           // 32 KB (2 atoms of 64 dims)
 constexpr int P_BYTES = BM * BN * 2;           // 32 KB (2 atoms of 64 keys)
 constexpr int ATOM = 128 * 128;                // bytes of one [128 rows x 128 B] swizzled box
-constexpr int SMEM = 1024 + Q_BYTES + 2 * K_BYTES + V_BYTES + P_BYTES + 256;
+constexpr int SMEM = 1024 + Q_BYTES + 2 * K_BYTES + V_BYTES + P_BYTES + 256 + 2048 + 64;
 constexpr float kRescaleThresh = 8.0f;         // log2 units
 
 struct Params {
@@ -57,13 +58,21 @@ CB_DEVICE uint64_t desc_mn_sw128(const void* p, uint32_t lbo, uint32_t sbo) {
   return d;
 }
 
+// 2^x with the hardware approximation (MUFU ex2, flush-to-zero); softmax inputs are <= 0 after the max shift.
+CB_DEVICE float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 CB_HOST_DEVICE uint32_t idesc_bf16_bmn(int M, int N) {  // A K-major, B MN-major
   return idesc_bf16(M, N) | (1u << 16);
 }
 
-__global__ void __launch_bounds__(256, 1) attn_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
-                                                              const __grid_constant__ CUtensorMap tm_k,
-                                                              const __grid_constant__ CUtensorMap tm_v,
+// tm_kv: the wkv_b output [T, H, 256] (k_nope dims 0..127 | v dims 128..255); tm_kpe: the shared RoPE key [T, 64].
+__global__ void __launch_bounds__(384, 1) attn_prefill_kernel(const __grid_constant__ CUtensorMap tm_q,
+                                                              const __grid_constant__ CUtensorMap tm_kv,
+                                                              const __grid_constant__ CUtensorMap tm_kpe,
                                                               const Params p) {
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 1000
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -82,7 +91,8 @@ __global__ void __launch_bounds__(256, 1) attn_prefill_kernel(const __grid_const
   uint64_t* s_empty = bars + 9;   // [2]
   uint64_t* p_full = bars + 11;
   uint64_t* pv_done = bars + 12;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
+  uint64_t* x_bar = bars + 13;    // [2] row-max / row-sum exchange between the two softmax halves
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int4 tile = p.tiles[blockIdx.x];
@@ -95,8 +105,9 @@ __global__ void __launch_bounds__(256, 1) attn_prefill_kernel(const __grid_const
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < 2; ++i) { mbar_init(&k_full[i], 1); mbar_init(&k_empty[i], 1);
-                                  mbar_init(&s_full[i], 1); mbar_init(&s_empty[i], 128); }
-    mbar_init(v_full, 1); mbar_init(v_empty, 1); mbar_init(p_full, 128); mbar_init(pv_done, 1);
+                                  mbar_init(&s_full[i], 1); mbar_init(&s_empty[i], 256); }
+    mbar_init(v_full, 1); mbar_init(v_empty, 1); mbar_init(p_full, 256); mbar_init(pv_done, 1);
+    mbar_init(&x_bar[0], 256); mbar_init(&x_bar[1], 256);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -109,24 +120,24 @@ __global__ void __launch_bounds__(256, 1) attn_prefill_kernel(const __grid_const
 
   if (warp == 0) {
     if (elect_one()) {
-      tma_prefetch_desc(&tm_q); tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_q); tma_prefetch_desc(&tm_kv); tma_prefetch_desc(&tm_kpe);
       mbar_arrive_expect_tx(q_full, Q_BYTES);
       for (int a = 0; a < 3; ++a) tma_load_3d(sQ + a * ATOM, &tm_q, q_full, a * 64, h, seq_start + q0);
       for (int j = 0; j < n_kt && !*abort_flag; ++j) {
         const int s = j & 1;
         if (!mbar_wait(&k_empty[s], ((j >> 1) & 1) ^ 1)) { fail(kErrTimeoutEmpty); break; }
         mbar_arrive_expect_tx(&k_full[s], K_BYTES);
-        for (int a = 0; a < 3; ++a)
-          tma_load_3d(sK + s * K_BYTES + a * ATOM, &tm_k, &k_full[s], a * 64, h, seq_start + j * BN);
+        for (int a = 0; a < 2; ++a)
+          tma_load_3d(sK + s * K_BYTES + a * ATOM, &tm_kv, &k_full[s], a * 64, h, seq_start + j * BN);
+        tma_load_2d(sK + s * K_BYTES + 2 * ATOM, &tm_kpe, &k_full[s], 0, seq_start + j * BN);
       }
     }
   } else if (warp == 3) {
     if (elect_one()) {
-      tma_prefetch_desc(&tm_v);
       for (int j = 0; j < n_kt && !*abort_flag; ++j) {
         if (!mbar_wait(v_empty, (j & 1) ^ 1)) { fail(kErrTimeoutEmpty); break; }
         mbar_arrive_expect_tx(v_full, V_BYTES);
-        for (int a = 0; a < 2; ++a) tma_load_3d(sV + a * ATOM, &tm_v, v_full, a * 64, h, seq_start + j * BN);
+        for (int a = 0; a < 2; ++a) tma_load_3d(sV + a * ATOM, &tm_kv, v_full, 128 + a * 64, h, seq_start + j * BN);
       }
     }
   } else if (warp == 1) {
@@ -171,81 +182,107 @@ __global__ void __launch_bounds__(256, 1) attn_prefill_kernel(const __grid_const
       }
     }
   } else if (warp >= 4) {
-    // ---------------- softmax / correction / epilogue ----------------
+    // ---------------- softmax / correction / epilogue: 8 warps, two per TMEM lane quadrant ----------------
+    // warp (4 + half*4 + q) owns rows 32q..32q+31 and score columns [64*half, 64*half + 64).
     const uint32_t q = warp & 3;
+    const int half = int(warp - 4) >> 2;
     const int row = q * 32 + lane;               // query row within the tile
     const int qi = q0 + row;                     // query index within the sequence
     const int tok = seq_start + qi;
     const uint32_t t_lane = tmem + ((q * 32) << 16);
+    // [2 parities][2 halves][128 rows]: row maxima, and after the loop the row sums
+    float* red = reinterpret_cast<float*>(const_cast<int*>(abort_flag) + 1);
+    auto exchange = [&](int it, float v, float& other) -> bool {
+      float* slot = red + (it & 1) * 256;
+      slot[half * 128 + row] = v;
+      mbar_arrive(&x_bar[it & 1]);
+      if (!mbar_wait(&x_bar[it & 1], (it >> 1) & 1)) return false;
+      other = slot[(half ^ 1) * 128 + row];
+      return true;
+    };
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kt; ++j) {
       const int s = j & 1;
       if (!mbar_wait(&s_full[s], (j >> 1) & 1)) { fail(kErrTimeoutTmem); ok = false; break; }
       tc_fence_after();
-      float sv[BN];
-#pragma unroll
-      for (int c = 0; c < BN; c += 32) {
+      float sv[64];
+      {
         uint32_t r[32];
-        tmem_ld_32x32b_x32(t_lane + s * 128 + c, r);
+        tmem_ld_32x32b_x32(t_lane + s * 128 + half * 64, r);
         tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) sv[c + i] = __uint_as_float(r[i]);
+        for (int i = 0; i < 32; ++i) sv[i] = __uint_as_float(r[i]);
+        tmem_ld_32x32b_x32(t_lane + s * 128 + half * 64 + 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sv[32 + i] = __uint_as_float(r[i]);
       }
       tc_fence_before();
       mbar_arrive(&s_empty[s]);
-      // mask + scale (log2 domain)
-      const int k0 = j * BN;
+      const int k0 = j * BN + half * 64;
       float mt = -INFINITY;
-      uint32_t words[BN / 32];
+      const bool dense_tile = (p.mask == nullptr) && (j * BN + BN - 1 <= q0);   // every key <= every query
+      if (dense_tile) {
 #pragma unroll
-      for (int w = 0; w < BN / 32; ++w)
-        words[w] = (p.mask && qi < seq_len && (k0 / 32 + w) < p.mask_words)
-                       ? p.mask[size_t(tok) * p.mask_words + k0 / 32 + w] : 0xffffffffu;
+        for (int i = 0; i < 64; ++i) mt = fmaxf(mt, sv[i]);
+        mt *= p.scale_log2;
+      } else {
+        uint32_t w0 = 0xffffffffu, w1 = 0xffffffffu;
+        if (p.mask && qi < seq_len) {
+          const int wi = k0 >> 5;
+          w0 = wi < p.mask_words ? p.mask[size_t(tok) * p.mask_words + wi] : 0u;
+          w1 = wi + 1 < p.mask_words ? p.mask[size_t(tok) * p.mask_words + wi + 1] : 0u;
+        }
 #pragma unroll
-      for (int i = 0; i < BN; ++i) {
-        const int kk = k0 + i;
-        const bool allowed = kk <= qi && ((words[i >> 5] >> (i & 31)) & 1u);
-        sv[i] = allowed ? sv[i] * p.scale_log2 : -INFINITY;
-        mt = fmaxf(mt, sv[i]);
+        for (int i = 0; i < 64; ++i) {
+          const uint32_t bit = ((i < 32 ? w0 : w1) >> (i & 31)) & 1u;
+          const bool allowed = (k0 + i <= qi) && bit;
+          sv[i] = allowed ? sv[i] : -INFINITY;
+          mt = fmaxf(mt, sv[i]);
+        }
+        mt = mt == -INFINITY ? mt : mt * p.scale_log2;
       }
-      // lazy rescale
-      bool need = (j > 0) && (mt > m_used + kRescaleThresh);
-      const float m_new = need || j == 0 ? fmaxf(m_used, mt) : m_used;
+      // row max across the two column halves
+      float mt_other;
+      if (!exchange(j, mt, mt_other)) { fail(kErrTimeoutTmem); ok = false; break; }
+      mt = fmaxf(mt, mt_other);
+      const bool need = (j > 0) && (mt > m_used + kRescaleThresh);
+      const float m_new = (need || j == 0) ? fmaxf(m_used, mt) : m_used;
       const float m_ref = m_new == -INFINITY ? 0.f : m_new;
       float alpha = 1.f;
-      if (need && m_used != -INFINITY) alpha = exp2f(m_used - m_ref);
+      if (need && m_used != -INFINITY) alpha = fast_exp2(m_used - m_ref);
       float rs = 0.f;
-      uint32_t pk[BN / 2];
+      uint32_t pk[32];
 #pragma unroll
-      for (int i = 0; i < BN; i += 2) {
-        const float a = exp2f(sv[i] - m_ref), b = exp2f(sv[i + 1] - m_ref);
+      for (int i = 0; i < 64; i += 2) {
+        const float a = fast_exp2(fmaf(sv[i], p.scale_log2, -m_ref));
+        const float b = fast_exp2(fmaf(sv[i + 1], p.scale_log2, -m_ref));
         rs += a + b;
         pk[i / 2] = pack_bf16x2(a, b);
       }
       l = l * alpha + rs;
       m_used = m_new;
-      // wait for the previous P·V (it reads P and accumulates into O)
       if (j > 0) {
         if (!mbar_wait(pv_done, (j - 1) & 1)) { fail(kErrTimeoutTmem); ok = false; break; }
         tc_fence_after();
         if (__any_sync(0xffffffffu, need)) {
 #pragma unroll 1
-          for (int c = 0; c < DV; c += 16) {
+          for (int c = 0; c < 64; c += 16) {
             uint32_t r[16];
-            tmem_ld_32x32b_x16(t_lane + 256 + c, r);
+            tmem_ld_32x32b_x16(t_lane + 256 + half * 64 + c, r);
             tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-            tmem_st_32x32b_x16(t_lane + 256 + c, r);
+            tmem_st_32x32b_x16(t_lane + 256 + half * 64 + c, r);
           }
           tmem_st_wait();
         }
       }
-      // P row -> shared memory (two 64-key swizzle atoms)
+      // P: this half's 64 keys form swizzle atom `half` of the P tile
 #pragma unroll
-      for (int c = 0; c < 16; ++c) {
-        uint8_t* dst = sP + (c >> 3) * ATOM + row * 128 + ((((c & 7) ^ (row & 7))) << 4);
+      for (int c = 0; c < 8; ++c) {
+        uint8_t* dst = sP + half * ATOM + row * 128 + ((c ^ (row & 7)) << 4);
         *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
       }
       fence_proxy_async();
@@ -255,14 +292,18 @@ __global__ void __launch_bounds__(256, 1) attn_prefill_kernel(const __grid_const
     if (ok && n_kt > 0) {
       if (!mbar_wait(pv_done, (n_kt - 1) & 1)) { fail(kErrTimeoutTmem); ok = false; }
     }
+    // full row sum = sum of the two halves' partial sums (alpha sequences are identical in both halves)
+    float l_other = 0.f;
+    if (ok && !exchange(n_kt, l, l_other)) { fail(kErrTimeoutTmem); ok = false; }
+    l += l_other;
     if (ok) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      __nv_bfloat16* o = p.out + (size_t(tok) * p.H + h) * DV;
+      __nv_bfloat16* o = p.out + (size_t(tok) * p.H + h) * DV + half * 64;
 #pragma unroll 1
-      for (int c = 0; c < DV; c += 32) {
+      for (int c = 0; c < 64; c += 32) {
         uint32_t r[32];
-        tmem_ld_32x32b_x32(t_lane + 256 + c, r);
+        tmem_ld_32x32b_x32(t_lane + 256 + half * 64 + c, r);
         tmem_ld_wait();
         if (qi < seq_len) {
 #pragma unroll
@@ -288,9 +329,10 @@ static bool make_tmap_3d(CUtensorMap* m, const void* ptr, uint64_t d0, uint64_t 
 
 }  // namespace fa
 
-// Host: q [T,H,192], k [T,H,192], v [T,H,128] bf16 contiguous; tiles [n_tiles] int4; out [T,H,128].
-cudaError_t attn_prefill(const void* q, const void* k, const void* v, int T, int H, const int* tiles, int n_tiles,
-                         const uint32_t* mask, int mask_words, float scale, void* out, int* status, cudaStream_t s);
+// Host: q [T,H,192], kvb [T,H,256] (k_nope | v), kpe [T,64] bf16 contiguous; tiles [n_tiles] int4; out [T,H,128].
+cudaError_t attn_prefill(const void* q, const void* kvb, const void* kpe, int T, int H, const int* tiles,
+                         int n_tiles, const uint32_t* mask, int mask_words, float scale, void* out, int* status,
+                         cudaStream_t s);
 
 }  // namespace cb
 
@@ -322,14 +364,16 @@ static bool make_tmap_3d(CUtensorMap* m, const void* ptr, uint64_t d0, uint64_t 
 }
 }  // namespace fa
 
-cudaError_t attn_prefill(const void* q, const void* k, const void* v, int T, int H, const int* tiles, int n_tiles,
-                         const uint32_t* mask, int mask_words, float scale, void* out, int* status, cudaStream_t s) {
+cudaError_t attn_prefill(const void* q, const void* kvb, const void* kpe, int T, int H, const int* tiles,
+                         int n_tiles, const uint32_t* mask, int mask_words, float scale, void* out, int* status,
+                         cudaStream_t s) {
   using namespace fa;
   if (n_tiles == 0) return cudaSuccess;
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tkv, tkpe;
   if (!make_tmap_3d(&tq, q, DQK, H, T, DQK * 2, uint64_t(H) * DQK * 2, 64, 1, BM) ||
-      !make_tmap_3d(&tk, k, DQK, H, T, DQK * 2, uint64_t(H) * DQK * 2, 64, 1, BN) ||
-      !make_tmap_3d(&tv, v, DV, H, T, DV * 2, uint64_t(H) * DV * 2, 64, 1, BN))
+      !make_tmap_3d(&tkv, kvb, 256, H, T, 256 * 2, uint64_t(H) * 256 * 2, 64, 1, BN) ||
+      !make_tmap_2d(&tkpe, kpe, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64, T, 64 * 2, 64, BN,
+                    CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
   static bool attr = false;
   if (!attr) {
@@ -346,7 +390,7 @@ cudaError_t attn_prefill(const void* q, const void* k, const void* v, int T, int
   p.out = reinterpret_cast<__nv_bfloat16*>(out);
   p.status = status;
   dim3 grid(n_tiles, H);
-  attn_prefill_kernel<<<grid, 256, SMEM, s>>>(tq, tk, tv, p);
+  attn_prefill_kernel<<<grid, 384, SMEM, s>>>(tq, tkv, tkpe, p);
   return cudaGetLastError();
 }
 

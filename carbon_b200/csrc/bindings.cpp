@@ -200,7 +200,8 @@ void gemm_fp8(torch::Tensor A, torch::Tensor sfa, torch::Tensor B, torch::Tensor
 
 void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor out, int64_t epi,
                c10::optional<torch::Tensor> m_block_expert, c10::optional<torch::Tensor> num_m_blocks,
-               int64_t N_per_group, c10::optional<torch::Tensor> status) {
+               int64_t N_per_group, c10::optional<torch::Tensor> status, int64_t k_splits) {
+  torch::Tensor work;
   CHECK_CUDA(A); CHECK_DT(A, at::kBFloat16); CHECK_DT(B, at::kBFloat16);
   TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && out.stride(-1) == 1);
   const int M = A.size(0), K = A.size(1), Nb = B.size(0);
@@ -208,24 +209,31 @@ void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor out, int64_t epi,
   const bool grouped = m_block_expert.has_value();
   const int N = grouped ? int(N_per_group) : Nb;
   if (epi == cb::GEMM_OUT_F32) { CHECK_DT(out, at::kFloat); } else { CHECK_DT(out, at::kBFloat16); }
+  if (k_splits > 1) {
+    TORCH_CHECK(epi == cb::GEMM_OUT_F32 && !grouped, "split-K needs fp32 output and a dense GEMM");
+    work = torch::empty({k_splits * int64_t(M) * out.stride(0)}, A.options().dtype(at::kFloat));
+  }
   c10::cuda::CUDAGuard g(A.device());
   CK(cb::gemm_bf16(A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0), M, N, K, Nb, out.data_ptr(), out.stride(0),
                    epi, ptr_or_null<const int>(m_block_expert), ptr_or_null<const int>(num_m_blocks),
-                   grouped ? m_block_expert->numel() : 0, ptr_or_null<int>(status), num_sms(), cur_stream()));
+                   grouped ? m_block_expert->numel() : 0, ptr_or_null<int>(status), num_sms(), cur_stream(),
+                   int(k_splits), k_splits > 1 ? work.data_ptr<float>() : nullptr));
 }
 
-void attn_prefill(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor tiles,
+// q [T, H, 192], kvb [T, H, 256] (k_nope | v), kpe [T, 64] -> out [T, H, 128]
+void attn_prefill(torch::Tensor q, torch::Tensor kvb, torch::Tensor kpe, torch::Tensor tiles,
                   c10::optional<torch::Tensor> mask, double scale, torch::Tensor out,
                   c10::optional<torch::Tensor> status) {
-  CHECK_CUDA(q); CHECK_DT(q, at::kBFloat16); CHECK_DT(k, at::kBFloat16); CHECK_DT(v, at::kBFloat16);
-  CHECK_CONTIG(q); CHECK_CONTIG(k); CHECK_CONTIG(v); CHECK_CONTIG(out); CHECK_DT(tiles, at::kInt);
-  TORCH_CHECK(q.size(2) == 192 && k.size(2) == 192 && v.size(2) == 128, "attn_prefill: head dims 192/128");
+  CHECK_CUDA(q); CHECK_DT(q, at::kBFloat16); CHECK_DT(kvb, at::kBFloat16); CHECK_DT(kpe, at::kBFloat16);
+  CHECK_CONTIG(q); CHECK_CONTIG(kvb); CHECK_CONTIG(kpe); CHECK_CONTIG(out); CHECK_DT(tiles, at::kInt);
+  TORCH_CHECK(q.size(2) == 192 && kvb.size(2) == 256 && kpe.size(-1) == 64, "attn_prefill: MLA dims 192/128");
   TORCH_CHECK(tiles.dim() == 2 && tiles.size(1) == 4);
   const int T = q.size(0), H = q.size(1);
+  TORCH_CHECK(kvb.size(0) == T && kvb.size(1) == H && kpe.numel() == int64_t(T) * 64);
   int words = 0;
   if (mask.has_value()) { CHECK_DT((*mask), at::kInt); TORCH_CHECK(mask->size(0) == T); words = mask->size(1); }
   c10::cuda::CUDAGuard g(q.device());
-  CK(cb::attn_prefill(q.data_ptr(), k.data_ptr(), v.data_ptr(), T, H, tiles.data_ptr<int>(), tiles.size(0),
+  CK(cb::attn_prefill(q.data_ptr(), kvb.data_ptr(), kpe.data_ptr(), T, H, tiles.data_ptr<int>(), tiles.size(0),
                       ptr_or_null<const uint32_t>(mask), words, float(scale), out.data_ptr(),
                       ptr_or_null<int>(status), cur_stream()));
 }
@@ -247,6 +255,25 @@ void topk_mask(torch::Tensor logits, int64_t Tq, int64_t k, torch::Tensor mask, 
   c10::cuda::CUDAGuard g(logits.device());
   CK(cb::topk_mask(logits.data_ptr<float>(), logits.stride(0), Tq, k, reinterpret_cast<uint32_t*>(mask.data_ptr()),
                    mask.size(1), row0, cur_stream()));
+}
+
+// q [T, H, 576], kv [S, 576] bf16, idx [T, K] int32 -> out [T, H, 512] bf16
+void sparse_mla(torch::Tensor q, torch::Tensor kv, torch::Tensor idx, double scale, int64_t n_splits,
+                c10::optional<torch::Tensor> work, torch::Tensor out) {
+  CHECK_CUDA(q); CHECK_DT(q, at::kBFloat16); CHECK_DT(kv, at::kBFloat16); CHECK_DT(idx, at::kInt);
+  CHECK_CONTIG(q); CHECK_CONTIG(kv); CHECK_CONTIG(idx); CHECK_CONTIG(out);
+  TORCH_CHECK(q.size(2) == 576 && kv.size(1) == 576 && out.size(2) == 512);
+  const int T = q.size(0), H = q.size(1);
+  float* po = nullptr;
+  float* pml = nullptr;
+  if (n_splits > 1) {
+    TORCH_CHECK(work.has_value() && work->numel() >= int64_t(T) * n_splits * H * 514, "sparse_mla: workspace");
+    po = work->data_ptr<float>();
+    pml = po + int64_t(T) * n_splits * H * 512;
+  }
+  c10::cuda::CUDAGuard g(q.device());
+  CK(cb::sparse_mla(q.data_ptr(), T, H, kv.data_ptr(), kv.size(0), idx.data_ptr<int>(), idx.size(1), float(scale),
+                    n_splits, po, pml, out.data_ptr(), nullptr, cur_stream()));
 }
 
 }  // namespace
@@ -276,4 +303,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_prefill", &attn_prefill);
   m.def("indexer_logits", &indexer_logits);
   m.def("topk_mask", &topk_mask);
+  m.def("sparse_mla", &sparse_mla);
 }

@@ -36,6 +36,24 @@ bool make_tmap_2d(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, int e
   return r == CUDA_SUCCESS;
 }
 
+__global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int M, int N, int ldo,
+                                     float* __restrict__ out) {
+  const int64_t total = int64_t(M) * N;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int r = int(i / N), c = int(i % N);
+    float acc = 0.f;
+    for (int sp = 0; sp < splits; ++sp) acc += part[(size_t(sp) * M + r) * ldo + c];
+    out[size_t(r) * ldo + c] = acc;
+  }
+}
+
+static cudaError_t splitk_reduce(const float* part, int splits, int M, int N, int ldo, float* out, cudaStream_t s) {
+  const int64_t total = int64_t(M) * N;
+  const int blocks = int(total / 256 + 1 < 1024 ? total / 256 + 1 : 1024);
+  splitk_reduce_kernel<<<blocks, 256, 0, s>>>(part, splits, M, N, ldo, out);
+  return cudaGetLastError();
+}
+
 template <int KIND, int EPI, int BN, int ST, int ACC>
 static cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int max_tiles,
                           int num_sms, cudaStream_t s) {
@@ -82,7 +100,7 @@ cudaError_t gemm_fp8(const void* A, const void* B, const uint32_t* sfa, const ui
 
 cudaError_t gemm_bf16(const void* A, int lda, const void* B, int ldb, int M, int N, int K, int Nb, void* out, int ldo,
                       int epi, const int* m_block_expert, const int* num_m_blocks_dev, int max_m_blocks, int* status,
-                      int num_sms, cudaStream_t s) {
+                      int num_sms, cudaStream_t s, int k_splits, float* work) {
   if (M <= 0 || N <= 0) return cudaSuccess;
   if (K % 64 || N % 16) return cudaErrorInvalidValue;
   constexpr int BN = 128;
@@ -98,7 +116,20 @@ cudaError_t gemm_bf16(const void* A, int lda, const void* B, int ldb, int M, int
   p.m_block_expert = m_block_expert; p.num_m_blocks_dev = num_m_blocks_dev; p.status = status;
   const int mblocks = m_block_expert ? max_m_blocks : ceil_div(M, 128);
   const int max_tiles = mblocks * ceil_div(N, BN);
-  if (epi == GEMM_OUT_F32) return launch<KIND_BF16, EPI_F32, 128, 6, 2>(ta, tb, p, max_tiles, num_sms, s);
+  if (epi == GEMM_OUT_F32) {
+    if (k_splits > 1) {
+      // partials [k_splits, M, ldo] in `work`, then an in-order reduction into `out`
+      if (m_block_expert || !work) return cudaErrorInvalidValue;
+      p.k_splits = k_splits;
+      p.out = work;
+      cudaError_t e = launch<KIND_BF16, EPI_F32, 128, 6, 2>(ta, tb, p, max_tiles * k_splits, num_sms, s);
+      if (e != cudaSuccess) return e;
+      const int nk_total = ceil_div(K, 64), nk_per = ceil_div(ceil_div(nk_total, k_splits), 4) * 4;
+      const int used = ceil_div(nk_total, nk_per);                     // splits that own at least one k-block
+      return splitk_reduce(work, used, M, N, ldo, reinterpret_cast<float*>(out), s);
+    }
+    return launch<KIND_BF16, EPI_F32, 128, 6, 2>(ta, tb, p, max_tiles, num_sms, s);
+  }
   return launch<KIND_BF16, EPI_BF16, 128, 6, 2>(ta, tb, p, max_tiles, num_sms, s);
 }
 
@@ -107,7 +138,7 @@ cudaError_t indexer_logits(const void* keys, int L, const void* q, int Tq, int H
                            int ldo, bool causal, int* status, int num_sms, cudaStream_t s) {
   if (L <= 0 || Tq <= 0) return cudaSuccess;
   constexpr int BN = 256;
-  if (Di % 64 || BN % H || H % 32) return cudaErrorInvalidValue;
+  if (Di % 64 || BN % H || H % 16) return cudaErrorInvalidValue;
   CUtensorMap ta, tb;
   if (!make_tmap_2d(&ta, keys, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Di, L, uint64_t(Di) * 2, 64, 128,
                     CU_TENSOR_MAP_SWIZZLE_128B) ||

@@ -41,6 +41,7 @@ struct GemmParams {
   const float* idx_w;          // [Tq, idx_heads]
   int idx_heads;
   int causal;                  // skip tiles whose first key is after their last query
+  int k_splits;                // EPI_F32 only: K split over CTAs; split s writes out + s*M*ldo (summed afterwards)
 };
 
 template <int BLOCK_N>
@@ -109,10 +110,13 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
   const int num_mb = grouped ? (p.num_m_blocks_dev ? *p.num_m_blocks_dev : ceil_div(p.M, BLOCK_M))
                              : ceil_div(p.M, BLOCK_M);
   const int num_nb = ceil_div(p.N, BLOCK_N);
-  const int num_tiles = num_mb * num_nb;
-  const int nk = ceil_div(p.K, BLOCK_K);
+  const int ksplit = (EPI == EPI_F32 && p.k_splits > 1) ? p.k_splits : 1;
+  const int num_tiles = num_mb * num_nb * ksplit;
+  const int nk_total = ceil_div(p.K, BLOCK_K);
+  const int nk_per = ceil_div(ceil_div(nk_total, ksplit), 4) * 4;   // whole SF groups per split
   constexpr int GROUP_M = 16;
   auto tile_coords = [&](int t, int& mb, int& nb) {
+    t /= ksplit;
     const int per_group = GROUP_M * num_nb;
     const int g = t / per_group, r = t - g * per_group;
     const int rows = min(GROUP_M, num_mb - g * GROUP_M);
@@ -124,7 +128,8 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
     *abort_flag = 1;
   };
   // causal tile skip (indexer): queries of tile nb are [nb*QPT, nb*QPT+QPT)
-  auto skip_tile = [&](int mb, int nb) -> bool {
+  auto skip_tile = [&](int mb, int nb, int t) -> bool {
+    if (ksplit > 1 && (t % ksplit) * nk_per >= nk_total) return true;   // empty K split
     if constexpr (EPI == EPI_INDEXER) {
       const int qpt = BLOCK_N / p.idx_heads;
       return p.causal && mb * BLOCK_M > nb * qpt + qpt - 1;
@@ -139,12 +144,13 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
       int stage = 0; uint32_t phase = 0;
       for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
         int mb, nb; tile_coords(t, mb, nb);
-        if (skip_tile(mb, nb)) continue;
+        if (skip_tile(mb, nb, t)) continue;
         int expert = 0;
         if (grouped) { expert = p.m_block_expert[mb]; if (expert < 0) continue; }
         const int a_row = mb * BLOCK_M;
         const int b_row = expert * p.N + nb * BLOCK_N;
-        for (int kb = 0; kb < nk; ++kb) {
+        const int kb0 = (t % ksplit) * nk_per, kb1 = min(nk_total, kb0 + nk_per);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1)) { fail(kErrTimeoutEmpty); break; }
           uint32_t bytes = S::TILE_A + S::TILE_B;
           if (kScaled && (kb & 3) == 0) {
@@ -168,7 +174,7 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
       int stage = 0; uint32_t phase = 0; int iter = 0;
       for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
         int mb, nb; tile_coords(t, mb, nb);
-        if (skip_tile(mb, nb)) continue;
+        if (skip_tile(mb, nb, t)) continue;
         if (grouped && p.m_block_expert[mb] < 0) continue;
         const int acc = iter % ACC_STAGES;
         const uint32_t acc_phase = (iter / ACC_STAGES) & 1;
@@ -176,7 +182,8 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BLOCK_N;
         bool ok = true;
-        for (int kb = 0; kb < nk; ++kb) {
+        const int kb0 = (t % ksplit) * nk_per, kb1 = min(nk_total, kb0 + nk_per);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase)) { fail(kErrTimeoutFull); ok = false; break; }
           tc_fence_after();
           if constexpr (kScaled) {
@@ -192,7 +199,7 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
 #pragma unroll
           for (int k = 0; k < kMmaPerStage; ++k) {
             const uint64_t koff = uint64_t((k * UMMA_K * kElemBytes) >> 4);  // advance inside the swizzle atom
-            const uint32_t accum = (kb > 0 || k > 0) ? 1u : 0u;
+            const uint32_t accum = (kb > kb0 || k > 0) ? 1u : 0u;
             if constexpr (kScaled) {
               const uint32_t sf_id = uint32_t(kb & 3);
               mma_mxf8_ss(d_tmem, a_desc + koff, b_desc + koff, idesc_mxf8(BLOCK_M, BLOCK_N, sf_id, sf_id),
@@ -216,7 +223,7 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
     int iter = 0;
     for (int t = blockIdx.x; t < num_tiles && !*abort_flag; t += gridDim.x) {
       int mb, nb; tile_coords(t, mb, nb);
-      if (skip_tile(mb, nb)) continue;
+      if (skip_tile(mb, nb, t)) continue;
       if (grouped && p.m_block_expert[mb] < 0) continue;
       const int acc = iter % ACC_STAGES;
       const uint32_t acc_phase = (iter / ACC_STAGES) & 1;
@@ -250,6 +257,10 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
               }
             } else {
               float* o = reinterpret_cast<float*>(p.out) + size_t(row) * p.ldo + col0;
+              if (ksplit > 1) {
+                // deterministic split-K: each split writes its own partial slab; a reduce kernel sums them in order
+                o += size_t(t % ksplit) * size_t(p.M) * p.ldo;
+              }
               if (col0 + 32 <= p.N && (p.ldo % 4) == 0) {
 #pragma unroll
                 for (int j = 0; j < 8; ++j)
@@ -269,12 +280,12 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
           const float* wq = p.idx_w + size_t(q_ok ? qi : 0) * p.idx_heads;
           float acc_l = 0.f;
 #pragma unroll 1
-          for (int c = 0; c < p.idx_heads; c += 32) {
-            uint32_t v[32];
-            tmem_ld_32x32b_x32(t_row + j * p.idx_heads + c, v);
+          for (int c = 0; c < p.idx_heads; c += 16) {
+            uint32_t v[16];
+            tmem_ld_32x32b_x16(t_row + j * p.idx_heads + c, v);
             tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) acc_l += wq[c + i] * fmaxf(__uint_as_float(v[i]), 0.f);
+            for (int i = 0; i < 16; ++i) acc_l += wq[c + i] * fmaxf(__uint_as_float(v[i]), 0.f);
           }
           if (row_ok && q_ok) {
             float* o = reinterpret_cast<float*>(p.out) + size_t(qi) * p.ldo + key;

@@ -42,16 +42,21 @@ cudaError_t gemm_fp8(const void* A, const void* B, const uint32_t* sfa, const ui
                      int num_sms, cudaStream_t s);
 cudaError_t gemm_bf16(const void* A, int lda, const void* B, int ldb, int M, int N, int K, int Nb, void* out, int ldo,
                       int epi, const int* m_block_expert, const int* num_m_blocks_dev, int max_m_blocks, int* status,
-                      int num_sms, cudaStream_t s);
+                      int num_sms, cudaStream_t s, int k_splits = 1, float* work = nullptr);
 
 // tcgen05 MLA prefill attention (attn_prefill.cu)
-cudaError_t attn_prefill(const void* q, const void* k, const void* v, int T, int H, const int* tiles, int n_tiles,
-                         const uint32_t* mask, int mask_words, float scale, void* out, int* status, cudaStream_t s);
+cudaError_t attn_prefill(const void* q, const void* kvb, const void* kpe, int T, int H, const int* tiles,
+                         int n_tiles, const uint32_t* mask, int mask_words, float scale, void* out, int* status,
+                         cudaStream_t s);
 
 // DSA indexer: logits GEMM with fused relu/weight/head-sum epilogue (gemm.cu) and exact top-k bitmask (topk.cu)
 cudaError_t indexer_logits(const void* keys, int L, const void* q, int Tq, int H, int Di, const float* w, float* out,
                            int ldo, bool causal, int* status, int num_sms, cudaStream_t s);
 cudaError_t topk_mask(const float* logits, int ldo, int Tq, int k, uint32_t* mask, int mask_words, int row0,
                       cudaStream_t s);
+
+// tcgen05 absorbed-MLA sparse attention over the latent cache (attn_decode.cu)
+cudaError_t sparse_mla(const void* q, int T, int H, const void* kv, int S, const int* idx, int K, float scale,
+                       int n_splits, float* part_o, float* part_ml, void* out, int* status, cudaStream_t s);
 
 }  // namespace cb

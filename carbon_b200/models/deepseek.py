@@ -331,12 +331,10 @@ class DeepseekModel:
         dn, dr, dv = cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.v_head_dim
         with region("attn.kv_up"):
             kvb = L.wkv_b(kv_c.to(self.act_dtype)).view(T, Hl, dn + dv)
-            k = torch.cat([kvb[..., :dn], k_pe.to(kvb.dtype).expand(T, Hl, dr)], dim=-1)
-            v = kvb[..., dn:].contiguous()
         with region("attn.indexer_topk"):
             masks = self._prefill_key_masks(idx_state, fb) if idx_state is not None else None
         with region("attn.core_prefill"):
-            return A.prefill_attention(q.contiguous(), k, v, fb.cu_seqlens, cfg.softmax_scale, masks)
+            return A.mla_prefill(q, kvb, k_pe.view(T, dr).to(kvb.dtype), fb.cu_seqlens, cfg.softmax_scale, masks)
 
     def _attn_decode(self, i, q, fb, cache, idx_state):
         cfg, L = self.cfg, self.layers[i]

@@ -24,37 +24,42 @@ from ._ext import ext
 
 
 def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens: List[int], scale: float,
-                      key_masks: Optional[List[Optional[torch.Tensor]]] = None) -> torch.Tensor:
+                      key_masks=None) -> torch.Tensor:
+    """Reference-layout entry: q [T,H,dqk], k [T,H,dqk], v [T,H,dv]."""
     T, H, dv = q.shape[0], q.shape[1], v.shape[2]
-    out = torch.empty(T, H, dv, dtype=q.dtype if q.is_cuda else torch.float32, device=q.device)
-    if q.is_cuda:
-        e = ext()
-        if hasattr(e, "attn_prefill") and q.shape[2] == 192 and v.shape[2] == 128:
-            mask = None
-            if isinstance(key_masks, torch.Tensor):
-                mask = key_masks                              # already packed [T, W] bits
-            elif key_masks is not None and any(m is not None for m in key_masks):
-                mask = pack_key_mask(key_masks, cu_seqlens, q.device)
-            tiles = prefill_tiles(cu_seqlens).to(q.device, non_blocking=True)
-            e.attn_prefill(q, k, v, tiles, mask, float(scale), out, None)
-            return out
+    if q.is_cuda and q.shape[2] == 192 and dv == 128:
+        dn = 128
+        kvb = torch.cat([k[..., :dn], v], dim=-1).contiguous()
+        kpe = k[:, 0, dn:].contiguous()
+        return mla_prefill(q, kvb, kpe, cu_seqlens, scale, key_masks)
+    out = torch.empty(T, H, dv, dtype=torch.float32, device=q.device)
     if isinstance(key_masks, torch.Tensor):
         key_masks = unpack_key_mask(key_masks, cu_seqlens)
     for b in range(len(cu_seqlens) - 1):
         s, t = cu_seqlens[b], cu_seqlens[b + 1]
         pos = torch.arange(t - s, device=q.device)
         m = key_masks[b] if key_masks is not None else None
-        if q.is_cuda:
-            # temporary path until the tcgen05 prefill kernel is registered (see attn_prefill)
-            allowed = torch.ones(t - s, t - s, dtype=torch.bool, device=q.device).tril_()
-            if m is not None:
-                allowed &= m
-            o = torch.nn.functional.scaled_dot_product_attention(
-                q[s:t].transpose(0, 1), k[s:t].transpose(0, 1), v[s:t].transpose(0, 1), attn_mask=allowed,
-                scale=scale)
-            out[s:t] = o.transpose(0, 1)
-        else:
-            out[s:t] = R.causal_attention(q[s:t], k[s:t], v[s:t], scale, pos, pos, m)
+        out[s:t] = R.causal_attention(q[s:t], k[s:t], v[s:t], scale, pos, pos, m)
+    return out
+
+
+def mla_prefill(q: torch.Tensor, kvb: torch.Tensor, kpe: torch.Tensor, cu_seqlens: List[int], scale: float,
+                key_masks=None) -> torch.Tensor:
+    """MLA prefill in the projection's own layout: q [T,H,192], kvb [T,H,256] = (k_nope | v) straight from the
+    wkv_b GEMM, kpe [T,64] the shared RoPE key (k = [k_nope, kpe] per head). Returns o [T,H,128]."""
+    T, H = q.shape[0], q.shape[1]
+    if not q.is_cuda:
+        dn = q.shape[2] - kpe.shape[-1]
+        k = torch.cat([kvb[..., :dn], kpe.view(T, 1, -1).expand(T, H, kpe.shape[-1])], dim=-1)
+        return prefill_attention(q, k, kvb[..., dn:], cu_seqlens, scale, key_masks)
+    mask = None
+    if isinstance(key_masks, torch.Tensor):
+        mask = key_masks
+    elif key_masks is not None and any(m is not None for m in key_masks):
+        mask = pack_key_mask(key_masks, cu_seqlens, q.device)
+    out = torch.empty(T, H, 128, dtype=torch.bfloat16, device=q.device)
+    tiles = prefill_tiles(cu_seqlens).to(q.device, non_blocking=True)
+    ext().attn_prefill(q.contiguous(), kvb.contiguous(), kpe.contiguous(), tiles, mask, float(scale), out, None)
     return out
 
 
@@ -102,6 +107,8 @@ def indexer_prefill_mask(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, cu_s
         return None
     T, W = cu_seqlens[-1], (max(lens) + 31) // 32
     if q.is_cuda:
+        if q.shape[1] % 16:
+            raise ValueError("the indexer kernel needs a multiple of 16 indexer heads")
         e = ext()
         mask = torch.empty(T, W, dtype=torch.int32, device=q.device)
         for a, b in zip(cu_seqlens[:-1], cu_seqlens[1:]):
@@ -121,14 +128,23 @@ def indexer_prefill_mask(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, cu_s
     return pack_key_mask(masks, cu_seqlens, q.device)
 
 
+def mla_splits(T: int, K: int, device) -> int:
+    """Key splits so that T x 2 (value halves) x splits CTAs fill the SMs; each split keeps >= 128 keys."""
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    s = max(1, sms // max(1, 2 * T))
+    return max(1, min(s, (K + 127) // 128))
+
+
 def sparse_mla(q: torch.Tensor, kv: torch.Tensor, idx: torch.Tensor, scale: float, d_latent: int) -> torch.Tensor:
     """Absorbed MQA over latent rows: q [T,H,D], kv [S,D], idx [T,K] int32 (-1 pad) -> o_lat [T,H,d_latent]."""
     T, H, D = q.shape
     if q.is_cuda:
         e = ext()
-        if hasattr(e, "sparse_mla"):
+        if hasattr(e, "sparse_mla") and D == 576 and d_latent == 512 and H <= 128:
             out = torch.empty(T, H, d_latent, dtype=torch.bfloat16, device=q.device)
-            e.sparse_mla(q, kv, idx, float(scale), out)
+            splits = mla_splits(T, idx.shape[1], q.device)
+            work = torch.empty(T * splits * H * 514, dtype=torch.float32, device=q.device) if splits > 1 else None
+            e.sparse_mla(q, kv, idx, float(scale), splits, work, out)
             return out
         # temporary path until the tcgen05 sparse-MLA kernel is registered
         sel = kv[idx.clamp(min=0).long()].float()                      # [T, K, D]

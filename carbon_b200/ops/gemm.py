@@ -51,8 +51,10 @@ def fp8_gemm_swiglu(a_q, a_sf, w13: Fp8Weight, limit: float = 0.0, m_block_exper
 
 
 def bf16_gemm(a: torch.Tensor, b: torch.Tensor, out_dtype=torch.bfloat16, out: Optional[torch.Tensor] = None,
-              m_block_expert=None, num_m_blocks=None, n_per_group: int = 0, status=None) -> torch.Tensor:
-    """a [M, K] bf16, b [N, K] bf16 -> a @ b.T."""
+              m_block_expert=None, num_m_blocks=None, n_per_group: int = 0, status=None,
+              k_splits: int = 0) -> torch.Tensor:
+    """a [M, K] bf16, b [N, K] bf16 -> a @ b.T.  fp32 output with few rows and long K is split over K across
+    CTAs (k_splits=0: automatic) so that a 1-tile problem still uses many SMs."""
     if not a.is_cuda:
         return (a.float() @ b.float().t()).to(out_dtype)
     M = a.shape[0]
@@ -60,7 +62,14 @@ def bf16_gemm(a: torch.Tensor, b: torch.Tensor, out_dtype=torch.bfloat16, out: O
     if out is None:
         out = torch.empty(M, N, dtype=out_dtype, device=a.device)
     epi = OUT_F32 if out.dtype == torch.float32 else OUT_BF16
-    ext().gemm_bf16(a, b, out, epi, m_block_expert, num_m_blocks, n_per_group, status)
+    if k_splits == 0:
+        k_splits = 1
+        if epi == OUT_F32 and m_block_expert is None:
+            tiles = ((M + 127) // 128) * ((N + 127) // 128)
+            kblocks = (a.shape[1] + 63) // 64
+            if tiles < 32 and kblocks >= 64:
+                k_splits = max(1, min(kblocks // 16, 128 // tiles))
+    ext().gemm_bf16(a, b, out, epi, m_block_expert, num_m_blocks, n_per_group, status, k_splits)
     return out
 
 

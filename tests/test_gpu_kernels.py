@@ -289,6 +289,7 @@ def test_attn_prefill(lens, masked):
     T = sum(lens)
     q = torch.randn(T, H, 192).to(torch.bfloat16)
     k = torch.randn(T, H, 192).to(torch.bfloat16)
+    k[..., 128:] = torch.randn(T, 1, 64).to(torch.bfloat16)       # MLA: one RoPE key shared by all heads
     v = torch.randn(T, H, 128).to(torch.bfloat16)
     cu = [0]
     for n in lens:
@@ -337,3 +338,33 @@ def test_topk_mask_exact(n, k):
     pos = torch.arange(n)
     exp = R.topk_mask(logits, pos, pos, k)
     assert torch.equal(got, exp)
+
+
+@pytest.mark.parametrize("T,H,K,S,splits_override", [(3, 128, 300, 1000, None), (16, 16, 64, 200, None),
+                                                      (2, 128, 2048, 5000, None), (40, 64, 100, 300, None)])
+def test_sparse_mla_decode(T, H, K, S, splits_override):
+    from carbon_b200.ops.attention import sparse_mla
+
+    torch.manual_seed(8)
+    q = (torch.randn(T, H, 576) * 0.5).to(torch.bfloat16)
+    kv = torch.randn(S, 576).to(torch.bfloat16)
+    idx = torch.randint(0, S, (T, K), dtype=torch.int32)
+    idx[:, -7:] = -1                       # padding
+    if T > 1:
+        idx[1, 5:] = -1                    # a short row
+    scale = 192 ** -0.5
+    out = sparse_mla(q.to(DEV), kv.to(DEV), idx.to(DEV), scale, 512)
+    torch.cuda.synchronize()
+    ref = sparse_mla(q.float(), kv.float(), idx, scale, 512)
+    assert rel_err(out, ref) < 1e-2, rel_err(out, ref)
+
+
+@pytest.mark.parametrize("M,N,K,splits", [(32, 64, 28672, 0), (5, 48, 4096, 7), (130, 128, 8192, 4)])
+def test_bf16_gemm_split_k(M, N, K, splits):
+    from carbon_b200.ops.gemm import bf16_gemm
+
+    torch.manual_seed(9)
+    a = torch.randn(M, K).to(torch.bfloat16)
+    b = torch.randn(N, K).to(torch.bfloat16)
+    out = bf16_gemm(a.to(DEV), b.to(DEV), out_dtype=torch.float32, k_splits=splits)
+    assert rel_err(out, a.float() @ b.float().t()) < 1e-5
