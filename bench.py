@@ -100,9 +100,9 @@ def reference_arm(args):
     """The reference is a set of slot bundles for a sealed SGLang-fork engine (sglang, deep_gemm 0.2.3, FlashMLA,
     torch 2.14+cu130) gated to sm_103; it has no installable package and cannot run offline here."""
     ref_dir = os.path.join(ROOT, "baseline", "_ref")
-    why = ("reference is slot bundles for a sealed SGLang-fork engine (needs sglang, deep_gemm 0.2.3.post2, "
-           "FlashMLA; levers gated to sm_103) with no pip-installable package; the install into baseline/_ref "
-           "failed offline")
+    why = ("pip install of the reference failed: 'not installable, neither setup.py nor pyproject.toml found'; it is "
+           "slot bundles for a sealed SGLang-fork engine (needs sglang, deep_gemm 0.2.3.post2, FlashMLA; levers "
+           "gated to sm_103), none of which is in the image")
     if os.path.isdir(ref_dir) and os.listdir(ref_dir):
         why = "baseline/_ref holds no importable engine: " + why
     line = {"impl": "reference", "unavailable": why}
