@@ -134,7 +134,8 @@ class Engine:
         rows = torch.tensor([c - 1 for c in cu[1:]], dtype=torch.int32)
         fb = ForwardBatch(ids=torch.tensor(ids, dtype=torch.int32).to(dev, non_blocking=True),
                           pos=pos.to(dev, non_blocking=True), out_loc=out_loc.to(dev, non_blocking=True),
-                          is_prefill=True, cu_seqlens=cu, logits_rows=rows.to(dev, non_blocking=True))
+                          is_prefill=True, cu_seqlens=cu, logits_rows=rows.to(dev, non_blocking=True),
+                          bounds=self._bounds(lens))
         logits = self.model.forward(fb, self.cache)
         for r, n in zip(reqs, lens):
             r.n_cached += n
@@ -158,12 +159,21 @@ class Engine:
         else:
             dev = self.device
             fb = ForwardBatch(ids=ids.to(dev), pos=pos.to(dev), out_loc=out_loc.to(dev), is_prefill=False,
-                              key_slots=key_slots.to(dev), n_keys=n_keys.to(dev))
+                              key_slots=key_slots.to(dev), n_keys=n_keys.to(dev), bounds=self._bounds([1] * bucket))
             logits = self.model.forward(fb, self.cache)[:B]
         for r in reqs:
             r.n_cached = r.seq_len
         self.stats["decode_tokens"] += B
         return logits
+
+    def _bounds(self, lengths):
+        """Per-rank token bounds (whole sequences per rank) when the model runs on several ranks."""
+        pc = self.model.pctx
+        if pc.world == 1:
+            return None
+        from ..parallel.dist import split_bounds
+
+        return split_bounds(list(lengths), pc.world)
 
     def _bucket(self, B: int) -> Optional[int]:
         for b in self.graph_buckets:
@@ -212,7 +222,7 @@ class _DecodeGraph:
         self.key_slots[:, 0] = 0
         self.n_keys = torch.ones(bucket, dtype=torch.int32, device=dev)
         fb = ForwardBatch(ids=self.ids, pos=self.pos, out_loc=self.out_loc, is_prefill=False,
-                          key_slots=self.key_slots, n_keys=self.n_keys)
+                          key_slots=self.key_slots, n_keys=self.n_keys, bounds=eng._bounds([1] * bucket))
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):

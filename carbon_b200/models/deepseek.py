@@ -115,6 +115,7 @@ class ForwardBatch:
     key_slots: Optional[torch.Tensor] = None  # decode: [B, Lmax] int32 slots of every key (incl. the new token)
     n_keys: Optional[torch.Tensor] = None     # decode: [B] int32
     logits_rows: Optional[torch.Tensor] = None  # rows that need logits (default: all)
+    bounds: Optional[List[int]] = None          # per-rank token shard bounds (multi-rank; sequence-aligned)
 
 
 class Layer:
@@ -271,83 +272,107 @@ class DeepseekModel:
     # attention
     # ------------------------------------------------------------------------------------------------------------------
     def attention(self, i: int, h: torch.Tensor, hq, fb: ForwardBatch, cache) -> torch.Tensor:
-        cfg, L = self.cfg, self.layers[i]
-        T, Hl = h.shape[0], self.H_local
+        """h: this rank's tokens [T_l, D]. Returns this rank's rows of the attention output [T_l, D]."""
+        cfg, L, pc = self.cfg, self.layers[i], self.pctx
+        Hl = self.H_local
         dn, dr, dv, r = cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.v_head_dim, cfg.kv_lora_rank
+        lo, hi = pc.local
+        pos_l = fb.pos[lo:hi]
         with region("attn.q_proj"):
             if cfg.q_lora_rank > 0:
                 q_lat_raw = L.wq_a(h, xq=hq)
-                if self.on_gpu:
-                    q_lat, q_lat_q = C.rms_norm(q_lat_raw, L.q_norm, cfg.rms_eps, want_bf16=True, want_fp8=True)
-                else:
-                    q_lat, q_lat_q = R.rms_norm(q_lat_raw, L.q_norm, cfg.rms_eps), None
-                q = L.wq_b(q_lat, xq=q_lat_q).view(T, Hl, dn + dr)
+                q_lat_l = C.rms_norm(q_lat_raw, L.q_norm, cfg.rms_eps) if self.on_gpu else \
+                    R.rms_norm(q_lat_raw, L.q_norm, cfg.rms_eps)
             else:
-                q_lat = h
-                q = L.wq(h, xq=hq).view(T, Hl, dn + dr)
+                q_lat_l = h
+        with region("attn.kv_proj"):
+            kv = L.wkv_a(h, xq=hq)                                                  # [T_l, r + dr]
+            kv_c = C.rms_norm(kv[:, :r].contiguous(), L.kv_norm, cfg.rms_eps) if self.on_gpu else \
+                R.rms_norm(kv[:, :r], L.kv_norm, cfg.rms_eps)
+            k_pe = kv[:, r:].contiguous().view(-1, 1, dr)
+            C.rope_(k_pe, 0, dr, self.cos_sin, pos_l)
+            latent_l = torch.cat([kv_c.to(self.act_dtype), k_pe.view(-1, dr).to(self.act_dtype)], dim=-1)
+        idx_l = None
+        if cfg.use_indexer:
+            with region("attn.indexer_qk"):
+                idx_l = self.indexer_qkw(i, h, q_lat_l, pos_l)
+        with region("tp.gather"):
+            q_lat = pc.gather_rows(q_lat_l.to(self.act_dtype) if self.on_gpu else q_lat_l)
+            latent = pc.gather_rows(latent_l)
+            idx_k = pc.gather_rows(idx_l[1]) if idx_l is not None else None
+        with region("attn.kv_proj"):
+            cache.write_latent(i, fb.out_loc, latent)
+            if idx_k is not None:
+                cache.write_index_k(i, fb.out_loc, idx_k)
+        T = q_lat.shape[0]
+        with region("attn.q_proj"):
+            if cfg.q_lora_rank > 0:
+                q = L.wq_b(q_lat).view(T, Hl, dn + dr)
+            else:
+                q = L.wq(q_lat).view(T, Hl, dn + dr)
             if not self.on_gpu:
                 q = q.clone()
             C.rope_(q, dn, dr, self.cos_sin, fb.pos)
-        with region("attn.kv_proj"):
-            kv = L.wkv_a(h, xq=hq)                                                  # [T, r + dr]
-            kv_c = C.rms_norm(kv[:, :r].contiguous(), L.kv_norm, cfg.rms_eps) if self.on_gpu else \
-                R.rms_norm(kv[:, :r], L.kv_norm, cfg.rms_eps)
-            k_pe = kv[:, r:].contiguous().view(T, 1, dr)
-            C.rope_(k_pe, 0, dr, self.cos_sin, fb.pos)
-            latent = torch.cat([kv_c.to(self.act_dtype), k_pe.view(T, dr).to(self.act_dtype)], dim=-1)
-            cache.write_latent(i, fb.out_loc, latent)
-        idx_state = None
-        if cfg.use_indexer:
-            with region("attn.indexer_qk"):
-                idx_state = self.indexer_qkw(i, h, q_lat, fb)
-                cache.write_index_k(i, fb.out_loc, idx_state[1])
         if fb.is_prefill:
-            o = self._attn_prefill(i, q, kv_c, k_pe, fb, idx_state, cache)
+            o = self._attn_prefill(i, q, latent, fb, idx_l, cache)
         else:
-            o = self._attn_decode(i, q, fb, cache, idx_state)
+            o = self._attn_decode(i, q, fb, cache, idx_l)
         with region("attn.o_proj"):
-            return L.wo(o.reshape(T, Hl * dv).to(self.act_dtype).contiguous())
+            part = L.wo(o.reshape(T, Hl * dv).to(self.act_dtype).contiguous())
+        with region("tp.reduce_scatter"):
+            return pc.reduce_scatter_rows(part)
 
-    def indexer_qkw(self, i, h, q_lat, fb):
+    def indexer_qkw(self, i, h, q_lat, pos):
         cfg, L = self.cfg, self.layers[i]
         T, Hi, Di, dr = h.shape[0], cfg.index_n_heads, cfg.index_head_dim, cfg.qk_rope_head_dim
         q = L.idx_wq(q_lat).view(T, Hi, Di)
         if not self.on_gpu:
             q = q.clone()
-        C.rope_(q, 0, dr, self.cos_sin, fb.pos)
+        C.rope_(q, 0, dr, self.cos_sin, pos)
         k = F.layer_norm(L.idx_wk(h).float(), (Di,), L.idx_kn_w, L.idx_kn_b, 1e-6).to(self.act_dtype)
         k = k.view(T, 1, Di)
-        C.rope_(k, 0, dr, self.cos_sin, fb.pos)
+        C.rope_(k, 0, dr, self.cos_sin, pos)
         w = (L.idx_wp(h, out_dtype=torch.float32) * (Hi ** -0.5) * (Di ** -0.5)).float()
         return q, k.view(T, Di), w
 
-    def _prefill_key_masks(self, idx_state, fb: ForwardBatch):
-        q, k, w = idx_state
-        return A.indexer_prefill_mask(q, k, w, fb.cu_seqlens, self.cfg.index_topk)
+    def _prefill_key_masks(self, idx_l, fb: ForwardBatch):
+        """DSA selection of this rank's sequences, gathered to all ranks (rows in global token order)."""
+        pc = self.pctx
+        lo, hi = pc.local
+        cu_l = [c - lo for c in fb.cu_seqlens if lo <= c <= hi]
+        lmax = max(b - a for a, b in zip(fb.cu_seqlens[:-1], fb.cu_seqlens[1:]))
+        if lmax <= self.cfg.index_topk:
+            return None
+        q, k, w = idx_l
+        m = A.indexer_prefill_mask(q, k, w, cu_l if len(cu_l) > 1 else [0, 0], self.cfg.index_topk, lmax=lmax)
+        return pc.gather_rows(m)
 
-    def _attn_prefill(self, i, q, kv_c, k_pe, fb, idx_state, cache):
+    def _attn_prefill(self, i, q, latent, fb, idx_l, cache):
         cfg, L = self.cfg, self.layers[i]
         T, Hl = q.shape[0], self.H_local
-        dn, dr, dv = cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.v_head_dim
+        dn, dr, dv, r = cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.v_head_dim, cfg.kv_lora_rank
         with region("attn.kv_up"):
-            kvb = L.wkv_b(kv_c.to(self.act_dtype)).view(T, Hl, dn + dv)
+            kvb = L.wkv_b(latent[:, :r].contiguous()).view(T, Hl, dn + dv)
         with region("attn.indexer_topk"):
-            masks = self._prefill_key_masks(idx_state, fb) if idx_state is not None else None
+            masks = self._prefill_key_masks(idx_l, fb) if idx_l is not None else None
         with region("attn.core_prefill"):
-            return A.mla_prefill(q, kvb, k_pe.view(T, dr).to(kvb.dtype), fb.cu_seqlens, cfg.softmax_scale, masks)
+            return A.mla_prefill(q, kvb, latent[:, r:].contiguous(), fb.cu_seqlens, cfg.softmax_scale, masks)
 
-    def _attn_decode(self, i, q, fb, cache, idx_state):
-        cfg, L = self.cfg, self.layers[i]
+    def _attn_decode(self, i, q, fb, cache, idx_l):
+        cfg, L, pc = self.cfg, self.layers[i], self.pctx
         T, Hl = q.shape[0], self.H_local
         dn, r = cfg.qk_nope_head_dim, cfg.kv_lora_rank
         with region("attn.absorb_q"):
             q_abs = head_bmm(q[..., :dn], L.w_uk)                                    # [T, Hl, r]
             qf = torch.cat([q_abs.to(self.act_dtype), q[..., dn:].to(self.act_dtype)], dim=-1).contiguous()
         idx = fb.key_slots
-        if idx_state is not None and int(fb.key_slots.shape[1]) > cfg.index_topk:
+        if idx_l is not None and int(fb.key_slots.shape[1]) > cfg.index_topk:
             with region("attn.indexer_topk"):
-                qi, _, wi = idx_state
-                idx = A.indexer_topk(qi, wi, cache.index_k[i], fb.key_slots, fb.n_keys, cfg.index_topk)
+                lo, hi = pc.local
+                qi, _, wi = idx_l
+                sel = A.indexer_topk(qi, wi, cache.index_k[i], fb.key_slots[lo:hi].contiguous(),
+                                     fb.n_keys[lo:hi].contiguous(), cfg.index_topk)
+                idx = pc.gather_rows(sel)
         with region("attn.core_decode"):
             o_lat = A.sparse_mla(qf, cache.latent[i], idx.contiguous(), cfg.softmax_scale, r)   # [T, Hl, r]
         with region("attn.absorb_o"):
@@ -402,15 +427,18 @@ class DeepseekModel:
     # whole model
     # ------------------------------------------------------------------------------------------------------------------
     def embed_tokens(self, ids: torch.Tensor):
+        """ids: every token of the batch; returns this rank's residual streams [T_l, hc, D] (and Σx² on GPU)."""
         cfg = self.cfg
-        T = ids.shape[0]
-        if not self.on_gpu:
+        if not self.on_gpu and self.pctx.world == 1:
+            T = ids.shape[0]
             X = self.embed[ids.long()][:, None, :].expand(T, cfg.hc_mult, cfg.hidden_size).clone()
             return X, None
         return self.pctx.embed(self, ids)
 
     def forward(self, fb: ForwardBatch, cache) -> torch.Tensor:
         cfg = self.cfg
+        T_all = fb.ids.shape[0]
+        self.pctx.set_bounds(fb.bounds if fb.bounds is not None else [0, T_all])
         with region("embed"):
             X, sumsq = self.embed_tokens(fb.ids)
         for i in range(cfg.n_layers):
@@ -420,8 +448,6 @@ class DeepseekModel:
             with region("mhc.pre_norm"):
                 h, hq = self.pre_norm(X, pre, L.attn_norm, want_fp8=self.on_gpu)
             a = self.attention(i, h, hq, fb, cache)
-            with region("tp.attn_out"):
-                a = self.pctx.attn_out(a)
             self._tr(f"{i}.attn_in", h); self._tr(f"{i}.attn_pre", pre); self._tr(f"{i}.attn_out", a)
             with region("mhc.post_mix"):
                 X, sumsq = self.post_mix(X, a, post, comb)
@@ -436,31 +462,48 @@ class DeepseekModel:
                 X, sumsq = self.post_mix(X, f, post, comb)
             self._tr(f"{i}.X_ffn", X)
         with region("head"):
-            return self.logits(X, sumsq, fb.logits_rows)
+            return self.logits(X, sumsq, fb)
 
     def _tr(self, name, t):
         if self.trace is not None:
             self.trace.append((name, t.detach().float().cpu().clone()))
 
-    def logits(self, X, sumsq, rows: Optional[torch.Tensor]) -> torch.Tensor:
-        cfg = self.cfg
+    def logits(self, X, sumsq, fb: ForwardBatch) -> torch.Tensor:
+        """Final mHC head mix + norm for the requested rows of this rank, gathered, then the (vocab-parallel) head."""
+        cfg, pc = self.cfg, self.pctx
+        lo, hi = pc.local
+        rows = fb.logits_rows
+        counts = None
         if rows is not None:
-            X = X[rows.long()].contiguous()
-            sumsq = sumsq[rows.long()] if sumsq is not None else None
+            if pc.world > 1:
+                # prefill: one logits row per sequence; shards hold whole sequences
+                ends = fb.cu_seqlens[1:]
+                counts = [sum(1 for e in ends if pc.bounds[r] < e <= pc.bounds[r + 1]) for r in range(pc.world)]
+                local_rows = torch.tensor([e - 1 - lo for e in ends if lo < e <= hi], dtype=torch.long,
+                                          device=X.device)
+            else:
+                local_rows = rows.long()
+            X = X[local_rows].contiguous()
+            sumsq = sumsq[local_rows] if sumsq is not None else None
         if not self.on_gpu:
             pre = R.mhc_head_coeffs(X, self.head_hc.fn, self.head_hc.base, self.head_hc.scale, cfg.hc_eps,
                                     cfg.rms_eps)
             y = R.rms_norm(R.mhc_pre_mix(X, pre), self.norm_w, cfg.rms_eps)
-            return y @ self.head_w.w.t()
-        from ..ops._ext import ext
+        else:
+            from ..ops._ext import ext
 
-        T = X.shape[0]
-        mix = bf16_gemm(X.view(T, -1), self.head_hc.fn, out_dtype=torch.float32)
-        pre = torch.empty(T, 4, device=X.device)
-        ext().mhc_head_coeffs(mix, sumsq, self.head_hc.base, self.head_hc.scale, X.shape[1] * X.shape[2],
-                              cfg.hc_eps, cfg.rms_eps, pre)
-        y, _ = self.pre_norm(X, pre, self.norm_w, want_fp8=False)
-        return self.pctx.lm_head(self, y)
+            T = X.shape[0]
+            pre = torch.empty(T, 4, device=X.device)
+            if T > 0:
+                mix = bf16_gemm(X.view(T, -1), self.head_hc.fn, out_dtype=torch.float32)
+                ext().mhc_head_coeffs(mix, sumsq, self.head_hc.base, self.head_hc.scale, X.shape[1] * X.shape[2],
+                                      cfg.hc_eps, cfg.rms_eps, pre)
+            y, _ = self.pre_norm(X, pre, self.norm_w, want_fp8=False)
+        if pc.world > 1:
+            y = pc.gather_var(y, counts) if counts is not None else pc.gather_rows(y)
+        if not self.on_gpu and pc.world == 1:
+            return y @ self.head_w.w.t()
+        return pc.lm_head(self, y)
 
 
 def head_bmm(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:

@@ -73,11 +73,11 @@ def prefill_tiles(cu_seqlens: List[int], bm: int = 128) -> torch.Tensor:
     return torch.tensor(tiles, dtype=torch.int32).view(-1, 4)
 
 
-def pack_key_mask(key_masks, cu_seqlens, device) -> torch.Tensor:
-    """Per-sequence bool masks -> one uint32 bit matrix [T, ceil(Lmax/32)] (bit j of word w = key 32w+j)."""
+def pack_key_mask(key_masks, cu_seqlens, device, W: Optional[int] = None) -> torch.Tensor:
+    """Per-sequence bool masks -> one uint32 bit matrix [T, W] (bit j of word w = key 32w+j)."""
     T = cu_seqlens[-1]
-    Lmax = max(b - a for a, b in zip(cu_seqlens[:-1], cu_seqlens[1:]))
-    W = (Lmax + 31) // 32
+    Lmax = max([b - a for a, b in zip(cu_seqlens[:-1], cu_seqlens[1:])] + [1])
+    W = (Lmax + 31) // 32 if W is None else W
     bits = torch.zeros(T, W * 32, dtype=torch.bool, device=device)
     for b, m in enumerate(key_masks):
         s, t = cu_seqlens[b], cu_seqlens[b + 1]
@@ -98,14 +98,15 @@ def unpack_key_mask(words: torch.Tensor, cu_seqlens: List[int]) -> List[torch.Te
 
 
 def indexer_prefill_mask(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, cu_seqlens: List[int],
-                         topk: int) -> Optional[torch.Tensor]:
+                         topk: int, lmax: Optional[int] = None) -> Optional[torch.Tensor]:
     """DSA selection for a prefill batch: per sequence, logits of every (query, causal key) pair and exact top-k.
     q [T, Hi, Di], k [T, Di], w [T, Hi]. Returns packed bits [T, ceil(Lmax/32)] (None when no sequence exceeds
     top-k, i.e. attention stays dense causal)."""
     lens = [b - a for a, b in zip(cu_seqlens[:-1], cu_seqlens[1:])]
-    if max(lens) <= topk:
+    lmax = max(lens) if lmax is None else lmax
+    if lmax <= topk:
         return None
-    T, W = cu_seqlens[-1], (max(lens) + 31) // 32
+    T, W = cu_seqlens[-1], (lmax + 31) // 32
     if q.is_cuda:
         if q.shape[1] % 16:
             raise ValueError("the indexer kernel needs a multiple of 16 indexer heads")
@@ -125,7 +126,7 @@ def indexer_prefill_mask(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, cu_s
         pos = torch.arange(n)
         lg = R.indexer_logits(q[a:b], k[a:b], w[a:b])
         masks.append(R.topk_mask(lg, pos, pos, topk))
-    return pack_key_mask(masks, cu_seqlens, q.device)
+    return pack_key_mask(masks, cu_seqlens, q.device, W)
 
 
 def mla_splits(T: int, K: int, device) -> int:

@@ -30,13 +30,31 @@ class ParallelCtx:
     ep_rank: int = 0
     vocab_parallel: bool = False
     group: Optional[object] = None   # torch.distributed process group (NCCL) when world > 1
+    bounds: Optional[list] = None    # token shard bounds of the current batch ([0, T] on one rank)
 
     @staticmethod
     def single() -> "ParallelCtx":
         return ParallelCtx()
 
+    def set_bounds(self, bounds) -> None:
+        self.bounds = bounds
+
+    @property
+    def local(self):
+        return self.bounds[self.rank], self.bounds[self.rank + 1]
+
+    def gather_rows(self, x):
+        return x
+
+    def gather_var(self, x, counts):
+        return x
+
+    def reduce_scatter_rows(self, x):
+        return x
+
     # -- hooks (single rank) -----------------------------------------------------------------------------------------
     def embed(self, model, ids: torch.Tensor):
+        """ids: all tokens of the batch (one rank: all tokens are local)."""
         from ..ops._ext import ext
 
         cfg = model.cfg
