@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--layers", type=int, default=0, help="override layer count (0 = config's)")
     ap.add_argument("--mem-frac", type=float, default=0.62, help="HBM fraction for weights (rest: cache, acts)")
     ap.add_argument("--profile", action="store_true", help="print per-region device times (stderr)")
+    ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
+                    help="multi-GPU data movement: our NVLink kernels (fused) or the NCCL baseline")
     return ap.parse_args()
 
 
@@ -146,24 +148,44 @@ def main():
     cfg = PRESETS[args.config]()
     if args.layers:
         cfg = cfg.replace(n_layers=args.layers)
-    pctx = ParallelCtx.single() if world == 1 else __import__(
-        "carbon_b200.parallel.ep", fromlist=["make_ctx"]).make_ctx(rank, world)
+    P, S = args.prompts_per_gpu, args.prompt_len
+    B, ctx = args.decode_batch_per_gpu, args.context
+    if world == 1:
+        pctx = ParallelCtx.single()
+    elif args.comm == "nccl":
+        from carbon_b200.parallel.dist import DistCtx
+
+        pctx = DistCtx(rank, world)
+    else:
+        from carbon_b200.parallel.fused import FusedCtx
+
+        max_tokens = max(P * S, B) * world
+        pctx = FusedCtx(rank, world, heap_bytes=heap_bytes(cfg, world, max_tokens, S), max_tokens=max_tokens,
+                        max_seq=S)
     mem = torch.cuda.get_device_properties(dev).total_memory
-    sets = pick_layer_sets(cfg, pctx.ep, mem, args.mem_frac)
+    page = 64
+    dec_pages = (B * world) * ((ctx + args.decode_steps * (args.warmup + args.steps) * 2 + 2 * page) // page + 1)
+    pf_pages = (P * world) * (S // page + 2)
+    num_pages = max(dec_pages, pf_pages) + 8
+    from carbon_b200.engine.kv_cache import PagedLatentCache
+
+    cache_b = num_pages * page * PagedLatentCache.bytes_per_token(cfg, cfg.n_layers)
+    heap_b = getattr(getattr(pctx, "heap", None), "nbytes", 0)
+    weight_budget = 0.90 * mem - cache_b - heap_b - (14 << 30)
+    sets = pick_layer_sets(cfg, pctx.ep, weight_budget / args.mem_frac, args.mem_frac)
     n_moe = cfg.n_layers - cfg.n_dense_layers
     tied = sets < n_moe
     src = WeightSource(cfg, seed=0, layer_sets=sets if tied else None)
     t0 = time.time()
-    P, S = args.prompts_per_gpu, args.prompt_len
-    B, ctx = args.decode_batch_per_gpu, args.context
-    page = 64
-    pages_needed = (B * ((ctx + args.decode_steps * (args.warmup + args.steps) + 2 * page) // page + 1) +
-                    P * (S // page + 2) + 8)
-    eng = Engine(cfg, device=dev, source=src, num_pages=pages_needed, page_size=page, cuda_graphs=True,
+    P, S = P * world, S                      # weak scaling: global prompts / decode batch grow with N
+    B = B * world
+    pages_needed = num_pages
+    graphs = world == 1 or args.comm == "fused"
+    eng = Engine(cfg, device=dev, source=src, num_pages=pages_needed, page_size=page, cuda_graphs=graphs,
                  graph_buckets=(B,), pctx=pctx)
     torch.cuda.synchronize()
     init_s = time.time() - t0
-    gen = torch.Generator().manual_seed(1234 + rank)
+    gen = torch.Generator().manual_seed(1234)     # SPMD: every rank builds the same requests
 
     def barrier():
         if world > 1:
@@ -247,21 +269,21 @@ def main():
     if world > 1:
         dist.barrier()
     if rank == 0:
-        pf_tok_s = P * S * world / (pf_ms / 1e3)
+        pf_tok_s = P * S / (pf_ms / 1e3)
         line = {
             "metric": METRIC, "value": round(pf_tok_s, 1), "unit": "tokens/s (prefill, whole job)",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(pf_ms, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp8 weights+GEMM inputs, "
             "bf16 activations", "data": "synthetic uniform-random token ids; random-init weights (N(0,0.02))",
-            "decode_out_tok_s": round(B * world / (dec_ms / 1e3), 1), "tpot_p50_ms": round(tpot_p50, 3),
+            "decode_out_tok_s": round(B / (dec_ms / 1e3), 1), "tpot_p50_ms": round(tpot_p50, 3),
             "decode_ms_per_step": round(dec_ms, 3),
-            "e2e": {"value": round(P * S * world / (e2e_ms / 1e3), 1), "unit": "tokens/s (prefill via Engine.prefill)",
+            "e2e": {"value": round(P * S / (e2e_ms / 1e3), 1), "unit": "tokens/s (prefill via Engine.prefill)",
                     "h2d_bytes_per_step": P * S * 4, "d2h_bytes_per_step": d2h // max(args.steps, 1)},
             "gpu_launches": launches,
             "clocks": clk.summary(),
             "config": {"model": f"{args.config} ({cfg.n_layers} layers, hidden {cfg.hidden_size}, "
                                 f"{cfg.n_routed_experts} experts top-{cfg.n_activated_experts})",
-                       "global_batch": P * world, "seq_len": S, "decode_batch": B * world, "context": ctx,
+                       "global_batch": P, "seq_len": S, "decode_batch": B, "context": ctx,
                        "parallelism": pctx_name(pctx, world),
                        "weights": (f"{sets} distinct MoE-layer weight sets cycled over {n_moe} MoE layers "
                                    "(every layer still runs; the full untied model needs 8 GPUs)") if tied
@@ -274,7 +296,23 @@ def main():
 
 
 def pctx_name(p, world):
-    return "single GPU" if world == 1 else f"tp{p.tp}-ep{p.ep}"
+    if world == 1:
+        return "single GPU"
+    kind = "NVLink peer-memory kernels" if type(p).__name__ == "FusedCtx" else "NCCL baseline"
+    return f"tp{p.tp} attention + ep{p.ep} MoE, sequence-sharded residual ({kind})"
+
+
+def heap_bytes(cfg, world, max_tokens, max_seq):
+    """Symmetric-heap size: reduce-scatter slots, MoE receive/output rows, gathers, vocab shard, slack."""
+    D = cfg.hidden_size
+    max_local = min(max_tokens, (max_tokens + world - 1) // world + max_seq)
+    rs = 2 * world * max_local * D * 2
+    cap = int(max_local * cfg.n_activated_experts * 1.6) + (cfg.n_routed_experts // world) * 128
+    moe = cap * D * 3 + cap * D // 32 + (1 << 20)
+    width = cfg.q_lora_rank + cfg.kv_lora_rank + cfg.qk_rope_head_dim + cfg.index_head_dim
+    gathers = 2 * 2 * max_tokens * (width * 2 + (max_seq // 32 + 1) * 4 + cfg.index_topk * 4)
+    emb = (cfg.vocab_size // world + 1) * D * 2
+    return int(rs + moe + gathers + emb + (1 << 30))
 
 
 def max_over_ranks(v: float, world: int) -> float:

@@ -279,9 +279,11 @@ void sparse_mla(torch::Tensor q, torch::Tensor kv, torch::Tensor idx, double sca
 }  // namespace
 
 void register_runtime(pybind11::module_& m);
+void register_p2p(pybind11::module_& m);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   register_runtime(m);
+  register_p2p(m);
   m.doc() = "carbon_b200 sm_100a kernels";
   m.def("act_quant", &act_quant);
   m.def("rms_norm", &rms_norm);

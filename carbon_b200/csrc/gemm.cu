@@ -133,6 +133,28 @@ cudaError_t gemm_bf16(const void* A, int lda, const void* B, int ldb, int M, int
   return launch<KIND_BF16, EPI_BF16, 128, 6, 2>(ta, tb, p, max_tiles, num_sms, s);
 }
 
+// o_proj GEMM fused with the reduce-scatter data movement: fp8 A [M,K] x B [N,K]^T, each output row stored into its
+// token owner's slot over NVLink (see EPI_BF16_SCATTER).
+cudaError_t gemm_fp8_scatter(const void* A, const void* B, const uint32_t* sfa, const uint32_t* sfb, int M, int N,
+                             int K, const uint64_t* scatter_ptrs, const int* bounds, int world, int my_rank,
+                             int slot_rows, int* status, int num_sms, cudaStream_t s) {
+  if (M <= 0 || N <= 0) return cudaSuccess;
+  if (K % 128 || N % 16 || N % 8) return cudaErrorInvalidValue;
+  CUtensorMap ta, tb;
+  if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, K, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, K, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  GemmParams p{};
+  p.M = M; p.N = N; p.K = K;
+  p.sfa = sfa; p.sfb = sfb;
+  p.sfa_row_blocks = ceil_div(M, 128);
+  p.sfb_row_blocks = ceil_div(N, 128);
+  p.ldo = N; p.status = status;
+  p.scatter_ptrs = scatter_ptrs; p.scatter_bounds = bounds; p.scatter_world = world; p.scatter_rank = my_rank;
+  p.scatter_rows = slot_rows;
+  return launch<KIND_MXF8, EPI_BF16_SCATTER, 128, 6, 2>(ta, tb, p, ceil_div(M, 128) * ceil_div(N, 128), num_sms, s);
+}
+
 // DSA indexer logits: keys [L, Di] bf16, q [Tq*H, Di] bf16, w [Tq, H] fp32 -> logits [Tq, ldo] fp32 (causal).
 cudaError_t indexer_logits(const void* keys, int L, const void* q, int Tq, int H, int Di, const float* w, float* out,
                            int ldo, bool causal, int* status, int num_sms, cudaStream_t s) {

@@ -21,7 +21,7 @@
 namespace cb {
 
 enum GemmKind { KIND_MXF8 = 0, KIND_BF16 = 1 };
-enum GemmEpi { EPI_BF16 = 0, EPI_SWIGLU_FP8 = 1, EPI_F32 = 2, EPI_INDEXER = 3 };
+enum GemmEpi { EPI_BF16 = 0, EPI_SWIGLU_FP8 = 1, EPI_F32 = 2, EPI_INDEXER = 3, EPI_BF16_SCATTER = 4 };
 
 struct GemmParams {
   int M, N, K;                 // N = per-expert N in grouped mode
@@ -42,6 +42,12 @@ struct GemmParams {
   int idx_heads;
   int causal;                  // skip tiles whose first key is after their last query
   int k_splits;                // EPI_F32 only: K split over CTAs; split s writes out + s*M*ldo (summed afterwards)
+  // EPI_BF16_SCATTER (GEMM -> reduce-scatter over NVLink): output row `row` belongs to the rank r with
+  // bounds[r] <= row < bounds[r+1]; it is stored straight into r's slot [my_rank] of its per-source partial buffer,
+  // scatter_ptrs[r] + (my_rank * slot_rows + row - bounds[r]) * ldo.
+  const uint64_t* scatter_ptrs;
+  const int* scatter_bounds;
+  int scatter_world, scatter_rank, scatter_rows;
 };
 
 template <int BLOCK_N>
@@ -232,7 +238,16 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
       const int row = mb * BLOCK_M + row_in_tile;
       const bool row_ok = row < p.M;
       const uint32_t t_row = tmem_base + ((q * 32) << 16) + acc * BLOCK_N;
-      if constexpr (EPI == EPI_BF16 || EPI == EPI_F32) {
+      if constexpr (EPI == EPI_BF16 || EPI == EPI_F32 || EPI == EPI_BF16_SCATTER) {
+        __nv_bfloat16* row_base = nullptr;
+        if constexpr (EPI == EPI_BF16_SCATTER) {
+          int r = 0;
+          while (r + 1 < p.scatter_world && row >= p.scatter_bounds[r + 1]) ++r;
+          row_base = reinterpret_cast<__nv_bfloat16*>(p.scatter_ptrs[r]) +
+                     (size_t(p.scatter_rank) * p.scatter_rows + (row - p.scatter_bounds[r])) * size_t(p.ldo);
+        } else if constexpr (EPI == EPI_BF16) {
+          row_base = reinterpret_cast<__nv_bfloat16*>(p.out) + size_t(row) * p.ldo;
+        }
 #pragma unroll 1
         for (int c = 0; c < BLOCK_N; c += 32) {
           uint32_t v[32];
@@ -240,8 +255,8 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
           tmem_ld_wait();
           const int col0 = nb * BLOCK_N + c;
           if (row_ok && col0 < p.N) {
-            if constexpr (EPI == EPI_BF16) {
-              __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(p.out) + size_t(row) * p.ldo + col0;
+            if constexpr (EPI == EPI_BF16 || EPI == EPI_BF16_SCATTER) {
+              __nv_bfloat16* o = row_base + col0;
               if (col0 + 32 <= p.N && (p.ldo % 8) == 0) {
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
@@ -340,6 +355,7 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
       mbar_arrive(&tempty_bar[acc]);
       ++iter;
     }
+    if constexpr (EPI == EPI_BF16_SCATTER) __threadfence_system();   // peer stores performed before any barrier
   }
 
   __syncthreads();

@@ -1,0 +1,330 @@
+// NVLink peer-memory kernels for the multi-GPU paths (symmetric heap, see symm.cu):
+//
+//  * p2p_gather_rows     : every rank writes its rows into every peer's gathered buffer (the all-gather of the
+//                          down-projection outputs / DSA selection), 16-byte P2P stores.
+//  * p2p_scatter_partials: rank s writes the rows of its o_proj partial sum that token-shard owner r holds into
+//                          r's slot [s]; reduce_slots sums the world slots locally in fp32 (the reduce-scatter).
+//  * EP MoE: moe_count (per-expert counts -> owners), moe_dispatch (fp8 1x128 quantisation of each token row fused
+//    with the P2P stores of the row and its UE8M0 scale bytes into the owner's expert-sorted receive buffer, in
+//    the SF-tile layout the grouped GEMM reads), moe_combine_pull (P2P loads of the expert outputs from their
+//    owners fused with the weighted top-k reduction and the shared-expert add).
+//  * embed_peer: vocab-parallel embedding — each token's row is read straight from its owner's table.
+//
+// Every kernel here only loads/stores peer memory with ordinary (non-TMA) instructions; the cross-rank ordering is
+// done by the signal/wait kernels of symm.cu (release/acquire at system scope, bounded waits).
+// Reference: MegaMoE dispatch/combine over SymBuffer (king_v10/bundle_v9/cuda_moe_prefill.py:4343-4660,
+// 5542-5681), Engram peer reads (cuda_peer_read.py:64-126).
+#include "common.cuh"
+
+namespace cb {
+
+// ---------------------------------------------------------------------------------------------------------------
+// all-gather of rows: src [n, row_bytes] -> dst_ptrs[r] + (row0 + i) * row_bytes for every rank r
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void p2p_gather_kernel(const uint8_t* __restrict__ src, int n, int row_bytes,
+                                  const uint64_t* __restrict__ dst_ptrs, int world, int row0) {
+  const int chunks = row_bytes / 16;
+  const int64_t total = int64_t(n) * chunks;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int64_t row = i / chunks, c = i % chunks;
+    const uint4 v = reinterpret_cast<const uint4*>(src + row * row_bytes)[c];
+    for (int r = 0; r < world; ++r) {
+      uint8_t* dst = reinterpret_cast<uint8_t*>(dst_ptrs[r]) + (row0 + row) * row_bytes;
+      reinterpret_cast<uint4*>(dst)[c] = v;
+    }
+  }
+  __threadfence_system();   // this thread's peer stores are performed before any later barrier publishes them
+}
+
+cudaError_t p2p_gather_rows(const void* src, int n, int row_bytes, const uint64_t* dst_ptrs, int world, int row0,
+                            cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  if (row_bytes % 16) return cudaErrorInvalidValue;
+  const int64_t total = int64_t(n) * (row_bytes / 16);
+  const int blocks = int(total / 256 + 1 < 4 * 148 ? total / 256 + 1 : 4 * 148);
+  p2p_gather_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const uint8_t*>(src), n, row_bytes, dst_ptrs, world,
+                                           row0);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// reduce-scatter: partial [T, D] bf16 -> owner r's slot buffer rows [my_rank][i] for rows of r's shard;
+// reduce_slots: out[i] = sum_s slots[s][i] (fp32 accumulate, bf16 out)
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void p2p_scatter_kernel(const __nv_bfloat16* __restrict__ part, int D, const int* __restrict__ bounds,
+                                   int world, int my_rank, const uint64_t* __restrict__ slot_ptrs, int slot_rows,
+                                   int T) {
+  const int chunks = D / 8;
+  const int64_t total = int64_t(T) * chunks;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int row = int(i / chunks), c = int(i % chunks);
+    int r = 0;
+    while (r + 1 < world && row >= bounds[r + 1]) ++r;
+    const int li = row - bounds[r];
+    const uint4 v = reinterpret_cast<const uint4*>(part + size_t(row) * D)[c];
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(slot_ptrs[r]) + (size_t(my_rank) * slot_rows + li) * D;
+    reinterpret_cast<uint4*>(dst)[c] = v;
+  }
+  __threadfence_system();
+}
+
+__global__ void reduce_slots_kernel(const __nv_bfloat16* __restrict__ slots, int world, int slot_rows, int n, int D,
+                                    __nv_bfloat16* __restrict__ out) {
+  const int chunks = D / 8;
+  const int64_t total = int64_t(n) * chunks;
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
+    const int row = int(i / chunks), c = int(i % chunks);
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int s = 0; s < world; ++s) {
+      const uint4 v = reinterpret_cast<const uint4*>(slots + (size_t(s) * slot_rows + row) * D)[c];
+      acc[0] += bf16_lo(v.x); acc[1] += bf16_hi(v.x); acc[2] += bf16_lo(v.y); acc[3] += bf16_hi(v.y);
+      acc[4] += bf16_lo(v.z); acc[5] += bf16_hi(v.z); acc[6] += bf16_lo(v.w); acc[7] += bf16_hi(v.w);
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]); o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]); o.w = pack_bf16x2(acc[6], acc[7]);
+    reinterpret_cast<uint4*>(out + size_t(row) * D)[c] = o;
+  }
+}
+
+cudaError_t p2p_scatter_partials(const void* part, int T, int D, const int* bounds_dev, int world, int my_rank,
+                                 const uint64_t* slot_ptrs, int slot_rows, cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  if (D % 8) return cudaErrorInvalidValue;
+  const int64_t total = int64_t(T) * (D / 8);
+  const int blocks = int(total / 256 + 1 < 4 * 148 ? total / 256 + 1 : 4 * 148);
+  p2p_scatter_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(part), D, bounds_dev, world,
+                                            my_rank, slot_ptrs, slot_rows, T);
+  return cudaGetLastError();
+}
+
+cudaError_t reduce_slots(const void* slots, int world, int slot_rows, int n, int D, void* out, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  const int64_t total = int64_t(n) * (D / 8);
+  const int blocks = int(total / 256 + 1 < 4 * 148 ? total / 256 + 1 : 4 * 148);
+  reduce_slots_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(slots), world, slot_rows, n, D,
+                                             reinterpret_cast<__nv_bfloat16*>(out));
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// EP MoE
+// ---------------------------------------------------------------------------------------------------------------
+// counts: one CTA per global expert scans this rank's (token, slot) pairs in order; pair_rank[i] = rank of pair i
+// among the pairs of its expert (token order, deterministic), and the expert's count is written into its owner's
+// count matrix cnt_ptrs[owner] -> int32 [world(src)][E_local].
+__global__ void moe_count_kernel(const int* __restrict__ ids, int Tk, int El, int my_rank,
+                                 const uint64_t* __restrict__ cnt_ptrs, int* __restrict__ pair_rank) {
+  __shared__ int sw[32];
+  const int e = blockIdx.x;
+  int base = 0;
+  for (int i0 = 0; i0 < Tk; i0 += blockDim.x) {
+    const int i = i0 + threadIdx.x;
+    const int hit = (i < Tk && ids[i] == e) ? 1 : 0;
+    // inclusive block scan of hit
+    int v = hit;
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, v, o);
+      if (lane >= o) v += n;
+    }
+    if (lane == 31) sw[wid] = v;
+    __syncthreads();
+    if (wid == 0) {
+      int x = lane < nw ? sw[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x += n;
+      }
+      if (lane < nw) sw[lane] = x;
+    }
+    __syncthreads();
+    const int incl = v + (wid > 0 ? sw[wid - 1] : 0);
+    if (hit) pair_rank[i] = base + incl - 1;
+    base += sw[nw - 1];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    int* dst = reinterpret_cast<int*>(cnt_ptrs[e / El]) + my_rank * El + (e % El);
+    *dst = base;
+    __threadfence_system();
+  }
+}
+
+cudaError_t moe_count(const int* ids, int Tk, int E, int world, int my_rank, const uint64_t* cnt_ptrs,
+                      int* pair_rank, cudaStream_t s) {
+  const int El = E / world;
+  moe_count_kernel<<<E, 512, 0, s>>>(ids, Tk, El, my_rank, cnt_ptrs, pair_rank);
+  return cudaGetLastError();
+}
+
+// Owner-side layout from the count matrix: segment start of each local expert (padded to 128 rows), the expert of
+// every 128-row block, and the row offset of each source inside each expert segment. cnt: [world][El].
+__global__ void moe_owner_layout_kernel(const int* __restrict__ cnt, int world, int El, int max_blocks,
+                                        int* __restrict__ src_off, int* __restrict__ m_block_expert,
+                                        int* __restrict__ num_blocks) {
+  if (threadIdx.x != 0) return;
+  int acc = 0, b = 0;
+  for (int e = 0; e < El; ++e) {
+    int n = 0;
+    for (int sr = 0; sr < world; ++sr) {
+      src_off[sr * El + e] = acc + n;
+      n += cnt[sr * El + e];
+    }
+    const int nb = (n + 127) / 128;
+    for (int j = 0; j < nb && b < max_blocks; ++j) m_block_expert[b++] = e;
+    acc += nb * 128;
+  }
+  num_blocks[0] = b;
+  for (int j = b; j < max_blocks; ++j) m_block_expert[j] = -1;
+}
+
+cudaError_t moe_owner_layout(const int* cnt, int world, int El, int max_blocks, int* src_off, int* m_block_expert,
+                             int* num_blocks, cudaStream_t s) {
+  moe_owner_layout_kernel<<<1, 32, 0, s>>>(cnt, world, El, max_blocks, src_off, m_block_expert, num_blocks);
+  return cudaGetLastError();
+}
+
+// Dispatch: one CTA (256 threads) per local token; the row is quantised once (1x128 UE8M0 blocks), then written to
+// each selected expert's owner at row  src_off_owner[my_rank][e_local] + pair_rank.  Destination rows are stored
+// in pos_out [T, k] (global row index inside the owner's buffer) for the combine.
+// recv_ptrs[r]: fp8 rows [cap, D]; sf_ptrs[r]: SF tiles of those rows (row blocks = cap/128); off_ptrs[r]: the
+// owner's src_off [world][El].
+__global__ void moe_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int D, const int* __restrict__ ids, int k,
+                                    int El, int my_rank, const int* __restrict__ pair_rank,
+                                    const uint64_t* __restrict__ recv_ptrs, const uint64_t* __restrict__ sf_ptrs,
+                                    const uint64_t* __restrict__ off_ptrs, int cap, int* __restrict__ pos_out,
+                                    int* __restrict__ status) {
+  const int t = blockIdx.x;
+  const int row_blocks = cap / 128;
+  __shared__ int s_dst[16], s_owner[16];
+  if (threadIdx.x < k) {
+    const int e = ids[t * k + threadIdx.x];
+    const int owner = e / El, el = e % El;
+    const int base = reinterpret_cast<const int*>(off_ptrs[owner])[my_rank * El + el];
+    int row = base + pair_rank[t * k + threadIdx.x];
+    if (row >= cap) { if (status) atomicCAS(status, 0, kErrBadArg); row = -1; }
+    s_dst[threadIdx.x] = row;
+    s_owner[threadIdx.x] = owner;
+    pos_out[t * k + threadIdx.x] = row;
+  }
+  __syncthreads();
+  // each group of 16 threads quantises one 128-column block (8 values per thread)
+  for (int col = threadIdx.x * 8; col < D; col += blockDim.x * 8) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(x + size_t(t) * D + col);
+    float v[8] = {bf16_lo(raw.x), bf16_hi(raw.x), bf16_lo(raw.y), bf16_hi(raw.y),
+                  bf16_lo(raw.z), bf16_hi(raw.z), bf16_lo(raw.w), bf16_hi(raw.w)};
+    float amax = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const uint32_t sb = ue8m0_for_amax(amax);
+    const float inv = ue8m0_inv(sb);
+    uint2 q;
+    q.x = pack_fp8x4(v[0] * inv, v[1] * inv, v[2] * inv, v[3] * inv);
+    q.y = pack_fp8x4(v[4] * inv, v[5] * inv, v[6] * inv, v[7] * inv);
+    const int kb = col / 128;
+    for (int j = 0; j < k; ++j) {
+      const int row = s_dst[j];
+      if (row < 0) continue;
+      uint8_t* dst = reinterpret_cast<uint8_t*>(recv_ptrs[s_owner[j]]) + size_t(row) * D + col;
+      *reinterpret_cast<uint2*>(dst) = q;
+      if ((threadIdx.x & 15) == 0) {
+        const int rb = row >> 7, r = row & 127;
+        uint8_t* sfb = reinterpret_cast<uint8_t*>(sf_ptrs[s_owner[j]]) +
+                       ((size_t(kb >> 2) * row_blocks + rb) * 128 + (r & 31) * 4 + (r >> 5)) * 4 + (kb & 3);
+        *sfb = uint8_t(sb);
+      }
+    }
+  }
+  __threadfence_system();
+}
+
+cudaError_t moe_dispatch(const void* x, int T, int D, const int* ids, int k, int El, int my_rank,
+                         const int* pair_rank, const uint64_t* recv_ptrs, const uint64_t* sf_ptrs,
+                         const uint64_t* off_ptrs, int cap, int* pos_out, int* status, cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  if (D % 128 || k > 16 || cap % 128) return cudaErrorInvalidValue;
+  moe_dispatch_kernel<<<T, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), D, ids, k, El, my_rank, pair_rank,
+                                        recv_ptrs, sf_ptrs, off_ptrs, cap, pos_out, status);
+  return cudaGetLastError();
+}
+
+// Combine: out[t] = add[t] + sum_j w[t,j] * y_owner(j)[pos[t,j]] — P2P loads from the owners' output buffers.
+__global__ void moe_combine_pull_kernel(const uint64_t* __restrict__ y_ptrs, int D, const int* __restrict__ ids,
+                                        const int* __restrict__ pos, const float* __restrict__ w, int k, int El,
+                                        const __nv_bfloat16* __restrict__ add, __nv_bfloat16* __restrict__ out) {
+  const int t = blockIdx.x;
+  for (int c = threadIdx.x * 8; c < D; c += blockDim.x * 8) {
+    float acc[8];
+    if (add) {
+      const uint4 a = *reinterpret_cast<const uint4*>(add + size_t(t) * D + c);
+      acc[0] = bf16_lo(a.x); acc[1] = bf16_hi(a.x); acc[2] = bf16_lo(a.y); acc[3] = bf16_hi(a.y);
+      acc[4] = bf16_lo(a.z); acc[5] = bf16_hi(a.z); acc[6] = bf16_lo(a.w); acc[7] = bf16_hi(a.w);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+    }
+    for (int j = 0; j < k; ++j) {
+      const int row = pos[t * k + j];
+      if (row < 0) continue;
+      const int owner = ids[t * k + j] / El;
+      const float wv = w[t * k + j];
+      const uint4 v = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(y_ptrs[owner]) +
+                                                      size_t(row) * D + c);
+      acc[0] += wv * bf16_lo(v.x); acc[1] += wv * bf16_hi(v.x); acc[2] += wv * bf16_lo(v.y);
+      acc[3] += wv * bf16_hi(v.y); acc[4] += wv * bf16_lo(v.z); acc[5] += wv * bf16_hi(v.z);
+      acc[6] += wv * bf16_lo(v.w); acc[7] += wv * bf16_hi(v.w);
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]); o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]); o.w = pack_bf16x2(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(out + size_t(t) * D + c) = o;
+  }
+}
+
+cudaError_t moe_combine_pull(const uint64_t* y_ptrs, int T, int D, const int* ids, const int* pos, const float* w,
+                             int k, int El, const void* add, void* out, cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  moe_combine_pull_kernel<<<T, 128, 0, s>>>(y_ptrs, D, ids, pos, w, k, El,
+                                            reinterpret_cast<const __nv_bfloat16*>(add),
+                                            reinterpret_cast<__nv_bfloat16*>(out));
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// vocab-parallel embedding from peer HBM: X[t, s, :] = table_owner(id)[id - owner*per] for all hc streams
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void embed_peer_kernel(const uint64_t* __restrict__ table_ptrs, int per, int world,
+                                  const int* __restrict__ ids, int D, int hc, __nv_bfloat16* __restrict__ X,
+                                  float* __restrict__ sumsq) {
+  __shared__ float red[32];
+  const int t = blockIdx.x;
+  const int id = ids[t];
+  int owner = id / per;
+  if (owner >= world) owner = world - 1;
+  const __nv_bfloat16* row = reinterpret_cast<const __nv_bfloat16*>(table_ptrs[owner]) + size_t(id - owner * per) * D;
+  float ss = 0.f;
+  for (int col = threadIdx.x * 8; col < D; col += blockDim.x * 8) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(row + col);
+    ss += bf16_lo(raw.x) * bf16_lo(raw.x) + bf16_hi(raw.x) * bf16_hi(raw.x) + bf16_lo(raw.y) * bf16_lo(raw.y) +
+          bf16_hi(raw.y) * bf16_hi(raw.y) + bf16_lo(raw.z) * bf16_lo(raw.z) + bf16_hi(raw.z) * bf16_hi(raw.z) +
+          bf16_lo(raw.w) * bf16_lo(raw.w) + bf16_hi(raw.w) * bf16_hi(raw.w);
+    for (int s = 0; s < hc; ++s) *reinterpret_cast<uint4*>(X + (size_t(t) * hc + s) * D + col) = raw;
+  }
+  ss = block_sum(ss, red);
+  if (threadIdx.x == 0 && sumsq) sumsq[t] = ss * hc;
+}
+
+cudaError_t embed_peer(const uint64_t* table_ptrs, int per, int world, const int* ids, int T, int D, int hc,
+                       void* X, float* sumsq, cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  embed_peer_kernel<<<T, 128, 0, s>>>(table_ptrs, per, world, ids, D, hc, reinterpret_cast<__nv_bfloat16*>(X),
+                                      sumsq);
+  return cudaGetLastError();
+}
+
+}  // namespace cb

@@ -1,0 +1,134 @@
+"""Checkpoints in the DeepSeek block-scaled fp8 format (safetensors).
+
+* A quantised linear weight ``<name>`` is stored as float8_e4m3fn [N, K] next to ``<name>_scale_inv`` — fp32
+  [ceil(N/128), ceil(K/128)], the value that multiplies each 128×128 block (DeepSeek-V3's ``weight_scale_inv``).
+* Everything else (norms, router, mHC parameters, embedding, head) is stored in bf16 / fp32 as is.
+* Experts may be stored stacked (``ffn.experts.w1`` [E, I, D]) or per expert (``ffn.experts.{e}.w1``); both load.
+
+``save_checkpoint`` writes this format from a state dict (quantising the fp8 names with ``ref.ops.quant_fp8_blocks``,
+so scales are powers of two); ``CheckpointSource`` is a ``WeightSource`` that reads it lazily, dequantising on the
+target device.  The reference receives its weights from the sealed engine in the same fp8 + 128×128 block format
+(``king_v10/bundle_v9/placement.py:133-134``).
+"""
+from __future__ import annotations
+
+import json
+import os
+import re
+from typing import Dict, Iterable, Optional
+
+import torch
+
+from ..config import ModelConfig
+from ..ref import ops as R
+from .weights import WeightSource
+
+FP8_SUFFIXES = ("wq_a.weight", "wq_b.weight", "wkv_a.weight", "wkv_b.weight", "wo.weight", "ffn.w1", "ffn.w2",
+                "ffn.w3", "experts.w1", "experts.w2", "experts.w3", "shared.w1", "shared.w2", "shared.w3")
+_EXPERT_RE = re.compile(r"^(layers\.\d+\.ffn\.experts)\.(\d+)\.(w[123])$")
+
+
+def is_fp8_name(name: str) -> bool:
+    return name.endswith(FP8_SUFFIXES)
+
+
+def save_checkpoint(state: Dict[str, torch.Tensor], path: str, shard_bytes: int = 2 << 30,
+                    per_expert: bool = False) -> None:
+    """Write ``state`` (fp32 tensors) as fp8 block-scaled safetensors shards + an index JSON."""
+    from safetensors.torch import save_file
+
+    os.makedirs(path, exist_ok=True)
+    out: Dict[str, torch.Tensor] = {}
+    for name, t in state.items():
+        if is_fp8_name(name):
+            if t.dim() == 3:
+                mats = [(f"{name[:-3]}.{e}.{name[-2:]}" if per_expert else None, t[e]) for e in range(t.shape[0])]
+                if per_expert:
+                    for n2, m in mats:
+                        q, s = R.quant_fp8_blocks(m.float())
+                        out[n2], out[n2 + "_scale_inv"] = q, s
+                else:
+                    qs = [R.quant_fp8_blocks(m.float()) for _, m in mats]
+                    out[name] = torch.stack([q for q, _ in qs])
+                    out[name + "_scale_inv"] = torch.stack([s for _, s in qs])
+            else:
+                q, s = R.quant_fp8_blocks(t.float())
+                out[name], out[name + "_scale_inv"] = q, s
+        else:
+            out[name] = t.to(torch.bfloat16) if t.dim() >= 2 and t.numel() > 4096 else t.float()
+    index, shard, size, k = {}, {}, 0, 0
+
+    def flush():
+        nonlocal shard, size, k
+        if shard:
+            fn = f"model-{k:05d}.safetensors"
+            save_file({n: v.contiguous() for n, v in shard.items()}, os.path.join(path, fn))
+            for n in shard:
+                index[n] = fn
+            k += 1
+            shard, size = {}, 0
+
+    for n, v in out.items():
+        shard[n] = v
+        size += v.numel() * v.element_size()
+        if size >= shard_bytes:
+            flush()
+    flush()
+    with open(os.path.join(path, "model.safetensors.index.json"), "w") as f:
+        json.dump({"weight_map": index}, f)
+
+
+class CheckpointSource(WeightSource):
+    """WeightSource over a directory of safetensors shards (block-scaled fp8 names dequantised on load)."""
+
+    def __init__(self, cfg: ModelConfig, path: str, layer_sets: Optional[int] = None):
+        super().__init__(cfg, state=None, seed=0, layer_sets=layer_sets)
+        from safetensors import safe_open
+
+        self.path = path
+        idx = os.path.join(path, "model.safetensors.index.json")
+        if os.path.exists(idx):
+            with open(idx) as f:
+                wm = json.load(f)["weight_map"]
+        else:
+            wm = {}
+            for fn in sorted(os.listdir(path)):
+                if fn.endswith(".safetensors"):
+                    with safe_open(os.path.join(path, fn), "pt") as h:
+                        for n in h.keys():
+                            wm[n] = fn
+        self.weight_map = wm
+        self._handles = {}
+        self._safe_open = safe_open
+
+    def _tensor(self, name: str) -> torch.Tensor:
+        fn = self.weight_map[name]
+        h = self._handles.get(fn)
+        if h is None:
+            h = self._safe_open(os.path.join(self.path, fn), "pt")
+            self._handles[fn] = h
+        return h.get_tensor(name)
+
+    def has(self, name: str) -> bool:
+        return name in self.weight_map
+
+    def get(self, name: str, device, rows: Optional[slice] = None) -> torch.Tensor:
+        cname = self.canonical(name)
+        if cname not in self.weight_map and cname.endswith(("experts.w1", "experts.w2", "experts.w3")):
+            # per-expert storage: assemble the requested experts
+            base, w = cname.rsplit(".", 1)
+            E = self.cfg.n_routed_experts
+            rng = range(E) if rows is None else range(rows.start or 0, rows.stop if rows.stop is not None else E)
+            mats = [self._load(f"{base}.{e}.{w}", device) for e in rng]
+            return torch.stack(mats)
+        t = self._load(cname, device)
+        return t if rows is None else t[rows]
+
+    def _load(self, name: str, device) -> torch.Tensor:
+        t = self._tensor(name)
+        if t.dtype == torch.float8_e4m3fn:
+            s = self._tensor(name + "_scale_inv").float()
+            if t.dim() == 3:
+                return torch.stack([R.dequant_fp8_blocks(t[e].to(device), s[e].to(device)) for e in range(t.shape[0])])
+            return R.dequant_fp8_blocks(t.to(device), s.to(device))
+        return t.to(device=device, dtype=torch.float32)

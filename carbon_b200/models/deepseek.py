@@ -318,9 +318,7 @@ class DeepseekModel:
         else:
             o = self._attn_decode(i, q, fb, cache, idx_l)
         with region("attn.o_proj"):
-            part = L.wo(o.reshape(T, Hl * dv).to(self.act_dtype).contiguous())
-        with region("tp.reduce_scatter"):
-            return pc.reduce_scatter_rows(part)
+            return pc.row_parallel_out(L.wo, o.reshape(T, Hl * dv).to(self.act_dtype).contiguous())
 
     def indexer_qkw(self, i, h, q_lat, pos):
         cfg, L = self.cfg, self.layers[i]

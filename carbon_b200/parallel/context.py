@@ -52,6 +52,10 @@ class ParallelCtx:
     def reduce_scatter_rows(self, x):
         return x
 
+    def row_parallel_out(self, lin, x):
+        """Row-parallel projection (o_proj) of all tokens, reduced onto each token's owner rank."""
+        return self.reduce_scatter_rows(lin(x))
+
     # -- hooks (single rank) -----------------------------------------------------------------------------------------
     def embed(self, model, ids: torch.Tensor):
         """ids: all tokens of the batch (one rank: all tokens are local)."""

@@ -1,0 +1,213 @@
+"""Multi-rank execution over NVLink peer memory (the product path; ``dist.DistCtx`` is the NCCL baseline).
+
+Same sharding as ``DistCtx`` (sequence-sharded residual, TP attention, EP MoE, vocab-parallel embedding / head),
+but every data movement is one of this repo's kernels on the symmetric heap:
+
+* ``gather_rows``      — P2P stores of this rank's rows into every peer's gathered buffer (csrc/p2p.cu),
+* ``reduce_scatter_rows`` — P2P stores of the o_proj partial rows into their owner's per-source slot, then a local
+  fp32 sum of the slots,
+* ``moe``              — count -> owner layout -> dispatch fused with the fp8 quantisation (rows and UE8M0 scales
+  land in the owner's SF-tile layout) -> the owner's grouped tcgen05 GEMMs read them in place -> combine by P2P
+  loads fused with the weighted top-k sum and the shared-expert add,
+* ``embed``            — rows read straight from the owner's vocabulary shard in peer HBM.
+
+Ordering between ranks uses one device-epoch barrier kernel (release/acquire at system scope, bounded wait; graph
+capturable).  Gathered buffers are double-buffered per call site, which together with the barriers guarantees a
+rank never overwrites data a slower peer is still reading.
+"""
+from __future__ import annotations
+
+from typing import Dict, List, Optional
+
+import torch
+
+from ..ops._ext import ext
+from ..ops.gemm import fp8_gemm, fp8_gemm_swiglu
+from ..ops.quant import sf_words
+from .dist import DistCtx
+from .symm import SymmHeap
+
+
+class FusedCtx(DistCtx):
+    def __init__(self, rank: int, world: int, group=None, heap_bytes: int = 4 << 30, max_tokens: int = 8192,
+                 max_seq: int = 4096, moe_capacity: float = 1.6, barrier_timeout_s: float = 20.0):
+        super().__init__(rank, world, group)
+        self.device = torch.device("cuda", torch.cuda.current_device())
+        self.heap = SymmHeap(heap_bytes, rank, world, group, self.device)
+        self.max_tokens = max_tokens
+        self.max_local = min(max_tokens, (max_tokens + world - 1) // world + max_seq)
+        self.moe_capacity = moe_capacity
+        self.flags = self.heap.alloc((world,), torch.int32)
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.limit_ns = int(barrier_timeout_s * 1e9)
+        self._gather: Dict[str, list] = {}
+        self._parity: Dict[str, int] = {}
+        self._rs = None
+        self._moe = None
+        self._embed = None
+        self._bounds_dev = None
+        self._bounds_key = None
+
+    # -- primitives ------------------------------------------------------------------------------------------------
+    def barrier(self):
+        ext().p2p_barrier(self.flags.peers, self.rank, self.epoch, self.flags.local, self.status, self.limit_ns)
+
+    def check(self) -> int:
+        """Device status word (0 = ok; otherwise a timeout / capacity error code recorded by a kernel)."""
+        return int(self.status.item())
+
+    def _gbuf(self, key: str, row_shape, dtype, rows: int):
+        """Double-buffered gather slot for one call site; grows (power of two rows) when a call needs more rows.
+        Every rank sees the same sequence of shapes, so the heap layout stays symmetric."""
+        cur = self._gather.get(key)
+        if cur is None or cur[0].shape[0] < rows:
+            cap = 1 << max(4, (rows - 1).bit_length())
+            self._gather[key] = [self.heap.alloc((cap,) + tuple(row_shape), dtype) for _ in range(2)]
+            self._parity[key] = 0
+        bufs = self._gather[key]
+        p = self._parity[key]
+        self._parity[key] = p ^ 1
+        return bufs[p]
+
+    def gather_rows(self, x: torch.Tensor, key: str = "rows") -> torch.Tensor:
+        return self._gather_counts(x, self.counts(), key)
+
+    def gather_var(self, x: torch.Tensor, counts: List[int], key: str = "var") -> torch.Tensor:
+        return self._gather_counts(x, counts, key)
+
+    def _gather_counts(self, x: torch.Tensor, cnt: List[int], key: str) -> torch.Tensor:
+        T = sum(cnt)
+        row0 = sum(cnt[: self.rank])
+        b = self._gbuf(key + ":" + str(x.dtype) + str(tuple(x.shape[1:])), x.shape[1:], x.dtype, T)
+        if x.shape[0] > 0:
+            ext().p2p_gather_rows(x.contiguous(), b.peers, row0)
+        self.barrier()
+        return b.local[:T]
+
+    def _bounds_tensor(self):
+        key = tuple(self.bounds)
+        if self._bounds_key != key:
+            self._bounds_dev = torch.tensor(self.bounds, dtype=torch.int32, device=self.device)
+            self._bounds_key = key
+        return self._bounds_dev
+
+    def reduce_scatter_rows(self, x: torch.Tensor) -> torch.Tensor:
+        T, D = x.shape
+        buf = self._rs_buf(D)
+        n = self.counts()[self.rank]
+        if max(self.counts()) > self.max_local:
+            raise RuntimeError("reduce-scatter shard larger than the slot buffer")
+        ext().p2p_scatter_partials(x.to(torch.bfloat16).contiguous(), self._bounds_tensor(), self.rank, buf.peers,
+                                   self.max_local)
+        self.barrier()
+        out = torch.empty(n, D, dtype=torch.bfloat16, device=x.device)
+        ext().reduce_slots(buf.local, self.world, self.max_local, n, out)
+        return out
+
+    def _rs_buf(self, D: int):
+        if self._rs is None or self._rs[0].shape[2] != D:
+            self._rs = [self.heap.alloc((self.world, self.max_local, D), torch.bfloat16) for _ in range(2)]
+            self._rs_parity = 0
+        buf = self._rs[self._rs_parity]
+        self._rs_parity ^= 1
+        return buf
+
+    def row_parallel_out(self, lin, x):
+        """o_proj GEMM fused with the reduce-scatter: the GEMM epilogue stores each output row into its owner's slot
+        over NVLink; after one barrier the owner sums the world slots."""
+        if getattr(lin, "kind", None) != "fp8":
+            return self.reduce_scatter_rows(lin(x))
+        from ..ops.quant import quant_act
+
+        D = lin.out_features
+        buf = self._rs_buf(D)
+        if max(self.counts()) > self.max_local:
+            raise RuntimeError("reduce-scatter shard larger than the slot buffer")
+        q, sf = quant_act(x)
+        ext().gemm_fp8_scatter(q, sf, lin.fw.q, lin.fw.sf, buf.peers, self._bounds_tensor(), self.rank,
+                               self.max_local, self.status)
+        self.barrier()
+        n = self.counts()[self.rank]
+        out = torch.empty(n, D, dtype=torch.bfloat16, device=x.device)
+        ext().reduce_slots(buf.local, self.world, self.max_local, n, out)
+        return out
+
+    # -- model hooks -----------------------------------------------------------------------------------------------
+    def adopt_embedding(self, model):
+        """Move this rank's vocabulary shard into the heap so peers can read it."""
+        if self._embed is not None:
+            return
+        V, D = model.embed.shape
+        per = (model.cfg.vocab_size + self.world - 1) // self.world
+        b = self.heap.alloc((per, D), torch.bfloat16)
+        b.local[:V].copy_(model.embed)
+        model.embed = b.local[:V]
+        self._embed = (b, per)
+
+    def embed(self, model, ids_all: torch.Tensor):
+        self.adopt_embedding(model)
+        cfg = model.cfg
+        lo, hi = self.local
+        ids = ids_all[lo:hi].to(torch.int32).contiguous()
+        X = torch.empty(hi - lo, cfg.hc_mult, cfg.hidden_size, dtype=torch.bfloat16, device=ids.device)
+        sumsq = torch.empty(hi - lo, device=ids.device)
+        b, per = self._embed
+        ext().embed_peer(b.peers, per, ids, X, sumsq)
+        return X, sumsq
+
+    def _moe_bufs(self, model, T_l: int):
+        cfg = model.cfg
+        D, El, k = cfg.hidden_size, model.E_local, cfg.n_activated_experts
+        cap = int(self.max_local * k * self.moe_capacity) + El * 128
+        cap = (cap + 127) // 128 * 128
+        if self._moe is None:
+            h = self.heap
+            self._moe = {
+                "cnt": h.alloc((self.world, El), torch.int32),
+                "off": h.alloc((self.world, El), torch.int32),
+                "recv": h.alloc((cap, D), torch.float8_e4m3fn),
+                "sf": h.alloc((sf_words(cap, D),), torch.int32),
+                "y": h.alloc((cap, D), torch.bfloat16),
+                "cap": cap,
+                "mbe": torch.empty(cap // 128, dtype=torch.int32, device=self.device),
+                "nb": torch.empty(1, dtype=torch.int32, device=self.device),
+            }
+        return self._moe
+
+    def moe(self, model, L, h, w, ids, shared):
+        cfg = model.cfg
+        e = ext()
+        T, k = ids.shape
+        El, E = model.E_local, cfg.n_routed_experts
+        m = self._moe_bufs(model, T)
+        ids = ids.to(torch.int32).contiguous()
+        pair_rank = torch.empty(T * k, dtype=torch.int32, device=h.device)
+        e.moe_count(ids.view(-1), E, self.rank, m["cnt"].peers, pair_rank)
+        self.barrier()
+        e.moe_owner_layout(m["cnt"].local, self.world, El, m["off"].local, m["mbe"], m["nb"])
+        self.barrier()
+        pos = torch.empty(T, k, dtype=torch.int32, device=h.device)
+        e.moe_dispatch(h.contiguous(), ids, El, self.rank, pair_rank, m["recv"].peers, m["sf"].peers,
+                       m["off"].peers, m["cap"], pos, self.status)
+        self.barrier()
+        # owner: grouped GEMMs over the expert-sorted received rows, in place in the heap
+        I2 = 2 * cfg.moe_intermediate
+        act, act_sf = fp8_gemm_swiglu(m["recv"].local, m["sf"].local, L.e_w13, cfg.swiglu_limit, m["mbe"], m["nb"],
+                                      I2)
+        fp8_gemm(act, act_sf, L.e_w2, out=m["y"].local, m_block_expert=m["mbe"], num_m_blocks=m["nb"],
+                 n_per_group=cfg.hidden_size)
+        self.barrier()
+        out = torch.empty(T, cfg.hidden_size, dtype=torch.bfloat16, device=h.device)
+        e.moe_combine_pull(m["y"].peers, ids, pos, w.float().contiguous(), El, shared, out)
+        self.barrier()     # peers may not reuse `y` until every rank has pulled its rows
+        return out
+
+    def lm_head(self, model, y: torch.Tensor) -> torch.Tensor:
+        part = model.head_w(y, out_dtype=torch.float32)                     # [n, V/world]
+        per = (model.cfg.vocab_size + self.world - 1) // self.world
+        n = part.shape[0]
+        pad = torch.zeros(1, n * per, dtype=torch.float32, device=part.device)
+        pad.view(n, per)[:, : part.shape[1]] = part
+        g = self._gather_counts(pad, [1] * self.world, "logits%d" % n)        # [world, n*per]
+        return g.view(self.world, n, per).permute(1, 0, 2).reshape(n, self.world * per)[:, : model.cfg.vocab_size]

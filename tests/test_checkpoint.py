@@ -1,0 +1,41 @@
+"""fp8 block-scaled safetensors checkpoints: save -> load round trip; the engine served from a checkpoint equals
+the engine served from the same (fp8-rounded) weights in memory."""
+import torch
+
+from carbon_b200.config import tiny_config
+from carbon_b200.engine.engine import Engine
+from carbon_b200.models.checkpoint import CheckpointSource, is_fp8_name, save_checkpoint
+from carbon_b200.models.weights import WeightSource
+from carbon_b200.ref import ops as R
+from carbon_b200.ref.model import init_weights
+
+
+def _fp8_rounded(w):
+    out = {}
+    for k, v in w.items():
+        if is_fp8_name(k):
+            out[k] = torch.stack([R.dequant_fp8_blocks(*R.quant_fp8_blocks(x)) for x in v]) if v.dim() == 3 else \
+                R.dequant_fp8_blocks(*R.quant_fp8_blocks(v))
+        else:
+            out[k] = v
+    return out
+
+
+def test_checkpoint_roundtrip_and_engine(tmp_path):
+    cfg = tiny_config()
+    w = init_weights(cfg, seed=0)
+    for per_expert in (False, True):
+        d = tmp_path / f"ckpt{int(per_expert)}"
+        save_checkpoint(w, str(d), per_expert=per_expert)
+        src = CheckpointSource(cfg, str(d))
+        ref = _fp8_rounded(w)
+        for name in ("layers.0.attn.wq_b.weight", "layers.1.ffn.experts.w2", "layers.0.attn_hc.fn"):
+            got = src.get(name, "cpu")
+            exp = ref[name] if is_fp8_name(name) else ref[name].to(torch.bfloat16).float() \
+                if ref[name].numel() > 4096 else ref[name]
+            assert torch.allclose(got, exp, atol=1e-6), name
+    prompts = [[1, 2, 3, 4, 5, 6, 7, 8] * 4]
+    e1 = Engine(cfg, "cpu", source=CheckpointSource(cfg, str(tmp_path / "ckpt0")), num_pages=8, page_size=16)
+    st = {n: CheckpointSource(cfg, str(tmp_path / "ckpt0")).get(n, "cpu") for n in w}
+    e2 = Engine(cfg, "cpu", source=WeightSource(cfg, state=st), num_pages=8, page_size=16)
+    assert e1.generate(prompts, 4) == e2.generate(prompts, 4)

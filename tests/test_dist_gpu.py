@@ -1,0 +1,97 @@
+"""2-GPU engine: the NVLink peer-memory path (FusedCtx) and the NCCL baseline (DistCtx) against one GPU.
+
+TP attention over heads, EP MoE over experts (dispatch fused with fp8 quantisation, combine fused with the
+weighted top-k sum), vocab-parallel embedding read from peer HBM, sequence-sharded residual.  The partial o_proj
+sums cross the wire in bf16, so the bound is a small relative error rather than bit equality.
+"""
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _cfg():
+    from carbon_b200.config import small_gpu_config
+
+    return small_gpu_config().replace(n_layers=2, n_routed_experts=8, n_activated_experts=2, vocab_size=2048)
+
+
+def _prompts(cfg):
+    g = torch.Generator().manual_seed(5)
+    return [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (60, 300, 130)]
+
+
+def _worker(rank, world, port, comm, q):
+    from datetime import timedelta
+
+    from carbon_b200.engine.engine import Engine
+    from carbon_b200.models.weights import WeightSource
+    from carbon_b200.parallel.dist import DistCtx
+    from carbon_b200.parallel.fused import FusedCtx
+    from carbon_b200.ref.model import init_weights
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    try:
+        cfg = _cfg()
+        w = init_weights(cfg, seed=0)
+        if comm == "fused":
+            pctx = FusedCtx(rank, world, heap_bytes=1 << 30, max_tokens=1024, max_seq=512)
+        else:
+            pctx = DistCtx(rank, world)
+        eng = Engine(cfg, device=dev, source=WeightSource(cfg, state=w), num_pages=64, page_size=64, pctx=pctx)
+        outs, hist = eng.generate(_prompts(cfg), max_new_tokens=4, return_logits=True)
+        torch.cuda.synchronize()
+        status = pctx.check() if comm == "fused" else 0
+        q.put((rank, outs, [h.numpy().copy() for h in hist], status))
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("comm", ["fused", "nccl"])
+def test_two_gpu_engine_matches_single_gpu(comm):
+    from carbon_b200.engine.engine import Engine
+    from carbon_b200.models.weights import WeightSource
+    from carbon_b200.ref.model import init_weights
+
+    cfg = _cfg()
+    w = init_weights(cfg, seed=0)
+    single = Engine(cfg, device="cuda:0", source=WeightSource(cfg, state=w), num_pages=64, page_size=64)
+    _, hist_ref = single.generate(_prompts(cfg), max_new_tokens=4, return_logits=True)
+    del single
+    torch.cuda.empty_cache()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, comm, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=600) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    for rank, outs, hist, status in res:
+        assert status == 0, (rank, status)
+        for step, (a, b) in enumerate(zip(hist, hist_ref)):
+            a = torch.from_numpy(a)
+            rel = ((a - b).norm() / b.norm()).item()
+            assert rel < 0.03, (comm, rank, step, rel)
