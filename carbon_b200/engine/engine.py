@@ -166,6 +166,67 @@ class Engine:
         self.stats["decode_tokens"] += B
         return logits
 
+    def verify(self, reqs: List[Request], last_tokens: Sequence[int], drafts: List[List[int]]):
+        """Target verification of speculative drafts (the reference's DSpark 6-row verify, ``dec/gemm_tables.py:51``).
+
+        Each request appends ``last_token`` followed by its draft tokens; all rows run in ONE forward, every row
+        attending to the cache plus the rows before it. Greedy acceptance keeps the longest draft prefix the target
+        agrees with and adds the target's next token. Returns the accepted new tokens per request (>= 1 each).
+        KV rows of rejected drafts are simply overwritten later (positions are slot-addressed)."""
+        rows_pt, rows_len, ids = [], [], []
+        for r, t, d in zip(reqs, last_tokens, drafts):
+            base = r.seq_len
+            seq = [int(t)] + [int(x) for x in d]
+            self._ensure_pages(r, base + len(seq))
+            for j, tok in enumerate(seq):
+                rows_pt.append(r.pages)
+                rows_len.append(base + j + 1)
+                ids.append(tok)
+        n = len(ids)
+        out_loc, key_slots, n_keys, pos = decode_metadata(rows_pt, rows_len, self.page_size, n)
+        dev = self.device
+        fb = ForwardBatch(ids=torch.tensor(ids, dtype=torch.int32).to(dev), pos=pos.to(dev), out_loc=out_loc.to(dev),
+                          is_prefill=False, key_slots=key_slots.to(dev), n_keys=n_keys.to(dev),
+                          bounds=self._bounds([1] * n))
+        logits = self.model.forward(fb, self.cache)
+        pred = torch.argmax(logits.float(), dim=-1).tolist()
+        accepted, i = [], 0
+        for r, t, d in zip(reqs, last_tokens, drafts):
+            k = len(d) + 1
+            p = pred[i:i + k]
+            a = 0
+            while a < len(d) and p[a] == d[a]:
+                a += 1
+            new = [int(x) for x in d[:a]] + [p[a]]
+            r.out += [int(t)] + [int(x) for x in d[:a]]      # tokens whose KV is now valid in the cache
+            r.n_cached = r.seq_len
+            accepted.append(new)
+            i += k
+        self.stats["decode_tokens"] += n
+        return accepted
+
+    def generate_speculative(self, prompts: List[Sequence[int]], max_new_tokens: int, drafter=None, n_draft: int = 5):
+        """Greedy generation with draft-and-verify steps (``n_draft`` drafts + 1 row per request per step)."""
+        from .spec import NgramDrafter
+
+        drafter = drafter or NgramDrafter()
+        reqs = [self.add_request(p) for p in prompts]
+        logits = self.prefill(reqs)
+        pending = torch.argmax(logits.float(), dim=-1).tolist()       # next token of each request, not yet cached
+        produced = [[t] for t in pending]
+        self.stats.setdefault("verify_steps", 0)
+        while min(len(x) for x in produced) < max_new_tokens:
+            drafts = [drafter.propose(r.prompt + r.out + [t], n_draft) for r, t in zip(reqs, pending)]
+            acc = self.verify(reqs, pending, drafts)
+            self.stats["verify_steps"] += 1
+            for b, a in enumerate(acc):
+                produced[b] += a
+                pending[b] = a[-1]
+        outs = [p[:max_new_tokens] for p in produced]
+        for r in reqs:
+            self.release(r)
+        return outs
+
     def _bounds(self, lengths):
         """Per-rank token bounds (whole sequences per rank) when the model runs on several ranks."""
         pc = self.model.pctx
