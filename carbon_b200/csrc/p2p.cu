@@ -21,16 +21,17 @@ namespace cb {
 // ---------------------------------------------------------------------------------------------------------------
 // all-gather of rows: src [n, row_bytes] -> dst_ptrs[r] + (row0 + i) * row_bytes for every rank r
 // ---------------------------------------------------------------------------------------------------------------
+template <typename V>
 __global__ void p2p_gather_kernel(const uint8_t* __restrict__ src, int n, int row_bytes,
                                   const uint64_t* __restrict__ dst_ptrs, int world, int row0) {
-  const int chunks = row_bytes / 16;
+  const int chunks = row_bytes / int(sizeof(V));
   const int64_t total = int64_t(n) * chunks;
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
     const int64_t row = i / chunks, c = i % chunks;
-    const uint4 v = reinterpret_cast<const uint4*>(src + row * row_bytes)[c];
+    const V v = reinterpret_cast<const V*>(src + row * row_bytes)[c];
     for (int r = 0; r < world; ++r) {
       uint8_t* dst = reinterpret_cast<uint8_t*>(dst_ptrs[r]) + (row0 + row) * row_bytes;
-      reinterpret_cast<uint4*>(dst)[c] = v;
+      reinterpret_cast<V*>(dst)[c] = v;
     }
   }
   __threadfence_system();   // this thread's peer stores are performed before any later barrier publishes them
@@ -39,11 +40,16 @@ __global__ void p2p_gather_kernel(const uint8_t* __restrict__ src, int n, int ro
 cudaError_t p2p_gather_rows(const void* src, int n, int row_bytes, const uint64_t* dst_ptrs, int world, int row0,
                             cudaStream_t s) {
   if (n == 0) return cudaSuccess;
-  if (row_bytes % 16) return cudaErrorInvalidValue;
-  const int64_t total = int64_t(n) * (row_bytes / 16);
+  if (row_bytes % 4) return cudaErrorInvalidValue;
+  const bool wide = (row_bytes % 16) == 0;
+  const int64_t total = int64_t(n) * (row_bytes / (wide ? 16 : 4));
   const int blocks = int(total / 256 + 1 < 4 * 148 ? total / 256 + 1 : 4 * 148);
-  p2p_gather_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const uint8_t*>(src), n, row_bytes, dst_ptrs, world,
-                                           row0);
+  if (wide)
+    p2p_gather_kernel<uint4><<<blocks, 256, 0, s>>>(reinterpret_cast<const uint8_t*>(src), n, row_bytes, dst_ptrs,
+                                                    world, row0);
+  else
+    p2p_gather_kernel<uint32_t><<<blocks, 256, 0, s>>>(reinterpret_cast<const uint8_t*>(src), n, row_bytes,
+                                                       dst_ptrs, world, row0);
   return cudaGetLastError();
 }
 

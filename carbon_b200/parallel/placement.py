@@ -1,0 +1,77 @@
+"""Expert placement: relabel experts so that every EP rank carries a similar routed load.
+
+The reference fits a per-layer table offline and moves expert tensors with one NCCL all-to-all
+(``king_v10/bundle_v9/placement.py:47-128``, ``placement_table.py``).  Here:
+
+* ``ExpertLoad`` accumulates per-layer expert hit counts from the router output (host-side, cheap: one bincount
+  per MoE layer while enabled);
+* ``plan(load, ep)`` is a greedy longest-processing-time assignment: experts in decreasing load go to the rank
+  with the least load that still has a free slot.  It returns ``perm`` with ``perm[new_id] = old_id``; rank r
+  then owns new ids ``[r*El, (r+1)*El)``;
+* ``apply(model, layer, perm)`` permutes that layer's router rows, router bias and stacked expert weights in place,
+  so routing picks the new ids directly and the model computes exactly the same function.
+
+On several ranks the relabelled weights of a rank come from other ranks; ``redistribute`` moves them with one
+all-to-all per weight tensor (same mechanism as the reference).
+"""
+from __future__ import annotations
+
+from typing import Dict, List
+
+import torch
+
+
+class ExpertLoad:
+    def __init__(self, n_experts: int):
+        self.E = n_experts
+        self.counts: Dict[int, torch.Tensor] = {}
+
+    def record(self, layer: int, ids: torch.Tensor) -> None:
+        c = torch.bincount(ids.reshape(-1).long().cpu(), minlength=self.E)
+        self.counts[layer] = self.counts.get(layer, torch.zeros(self.E, dtype=torch.long)) + c
+
+
+def plan(load: torch.Tensor, ep: int) -> torch.Tensor:
+    """load [E] -> perm [E] (perm[new] = old) balancing the summed load of each rank's E/ep experts."""
+    E = load.numel()
+    El = E // ep
+    order = torch.argsort(load.float(), descending=True, stable=True).tolist()
+    rank_load = [0.0] * ep
+    slots: List[List[int]] = [[] for _ in range(ep)]
+    for e in order:
+        r = min((r for r in range(ep) if len(slots[r]) < El), key=lambda r: (rank_load[r], r))
+        slots[r].append(e)
+        rank_load[r] += float(load[e])
+    return torch.tensor([e for r in range(ep) for e in sorted(slots[r])], dtype=torch.long)
+
+
+def imbalance(load: torch.Tensor, ep: int, perm: torch.Tensor = None) -> float:
+    """max rank load / mean rank load for a placement (identity when perm is None)."""
+    l = load.float() if perm is None else load.float()[perm]
+    per = l.view(ep, -1).sum(1)
+    return float(per.max() / per.mean().clamp(min=1e-9))
+
+
+def apply(model, layer: int, perm: torch.Tensor) -> None:
+    """Relabel the experts of one MoE layer of a single-rank model (EP = 1) in place."""
+    L = model.layers[layer]
+    assert L.moe and model.pctx.ep == 1, "apply() relabels a single-rank model; use redistribute() across ranks"
+    p = perm.to(L.gate_b.device)
+    if L.gate.kind == "f32" or L.gate.kind == "bf16":
+        L.gate.w[: p.numel()] = L.gate.w[: p.numel()][p.to(L.gate.w.device)]
+    L.gate_b.copy_(L.gate_b[p])
+    if model.on_gpu:
+        from ..ops.quant import Fp8Weight, pack_sf
+
+        for name in ("e_w13", "e_w2"):
+            W = getattr(L, name)
+            E = p.numel()
+            rows = W.q.shape[0] // E
+            pq = p.to(W.q.device)
+            q = W.q.view(E, rows, -1)[pq].reshape(E * rows, -1).contiguous()
+            scale = W.scale.view(E, rows // 128, -1)[pq].reshape(E * rows // 128, -1).contiguous()
+            setattr(L, name, Fp8Weight(q, pack_sf(scale.repeat_interleave(128, dim=0)), scale))
+    else:
+        L.e_w1 = L.e_w1[p].contiguous()
+        L.e_w3 = L.e_w3[p].contiguous()
+        L.e_w2 = L.e_w2[p].contiguous()

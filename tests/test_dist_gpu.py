@@ -49,6 +49,7 @@ def _worker(rank, world, port, comm, q):
     torch.cuda.set_device(rank)
     dev = torch.device("cuda", rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
+    ok = False
     try:
         cfg = _cfg()
         w = init_weights(cfg, seed=0)
@@ -61,7 +62,12 @@ def _worker(rank, world, port, comm, q):
         torch.cuda.synchronize()
         status = pctx.check() if comm == "fused" else 0
         q.put((rank, outs, [h.numpy().copy() for h in hist], status))
+        ok = True
         dist.barrier()
+    except Exception as ex:               # report instead of leaving the parent waiting for a result
+        if not ok:
+            q.put((rank, None, repr(ex)[:2000], -1))
+        raise
     finally:
         dist.destroy_process_group()
 
@@ -85,7 +91,9 @@ def test_two_gpu_engine_matches_single_gpu(comm):
     procs = [ctx.Process(target=_worker, args=(r, 2, port, comm, q)) for r in range(2)]
     for p in procs:
         p.start()
-    res = [q.get(timeout=600) for _ in range(2)]
+    res = [q.get(timeout=420) for _ in range(2)]
+    for rank, outs, hist, status in res:
+        assert outs is not None, (rank, hist)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
