@@ -236,14 +236,19 @@ def main():
         eng._ensure_pages(r, r.seq_len)
         r.n_cached = ctx          # cache rows are synthetic: decode cost depends on context length, not content
         reqs.append(r)
-    nxt = [1] * B
+    # every decode step feeds fresh uniform-random token ids (synthetic data): routing stays as diverse as a real
+    # batch's, so each step streams the weights of every expert its tokens select
+    def next_ids():
+        return torch.randint(0, cfg.vocab_size, (B,), generator=gen).tolist()
+
     for _ in range(args.warmup):
         for _ in range(2):
-            eng.decode(reqs, nxt)
+            eng.decode(reqs, next_ids())
     barrier()
     step_ms = []
     for _ in range(args.steps):
         for _ in range(args.decode_steps):
+            nxt = next_ids()
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
             eng.decode(reqs, nxt)
@@ -263,7 +268,7 @@ def main():
         print("== prefill regions ==\n" + t.table(), file=sys.stderr, flush=True)
         eng.cuda_graphs = False
         with tracing() as t:
-            eng.decode(reqs, nxt)
+            eng.decode(reqs, next_ids())
         eng.cuda_graphs = True
         print("== decode regions (eager) ==\n" + t.table(), file=sys.stderr, flush=True)
     if world > 1:

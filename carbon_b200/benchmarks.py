@@ -158,14 +158,81 @@ def bench_decode_attn(a):
                       "tflops": round(T * H * K * (576 + 512) * 2 / ms / 1e9, 1), "peak_src": pk["src"]}))
 
 
+def bench_moe(a):
+    """Config 4 MoE layer (router top-k + routed experts + shared expert) on one GPU, or EP over all ranks of a
+    torchrun job (``--comm fused|nccl``): 256 experts top-8 + 1 shared, hidden 7168, intermediate 2048, fp8
+    block-scaled weights ~N(0, 0.02); router logits ~N(0,1) + per-expert bias ~N(0, 0.5) (Zipf-like skew)."""
+    import torch.distributed as dist
+
+    from .config import ModelConfig
+    from .models.deepseek import DeepseekModel
+    from .models.weights import WeightSource
+    from .parallel.context import ParallelCtx
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", torch.cuda.current_device()))
+    cfg = ModelConfig(n_layers=1, n_dense_layers=0, vocab_size=1024, n_routed_experts=a.experts,
+                      n_activated_experts=a.moe_topk, hidden_size=a.hidden, moe_intermediate=a.inter, index_n_heads=0)
+    if world == 1:
+        pctx = ParallelCtx.single()
+    elif a.comm == "nccl":
+        from .parallel.dist import DistCtx
+
+        pctx = DistCtx(rank, world)
+    else:
+        from .parallel.fused import FusedCtx
+
+        pctx = FusedCtx(rank, world, heap_bytes=12 << 30, max_tokens=a.tokens * world, max_seq=a.tokens)
+    model = DeepseekModel(cfg, WeightSource(cfg, seed=0), "cuda", pctx=pctx)
+    L = model.layers[0]
+    T = a.tokens
+    g = torch.Generator(device="cuda").manual_seed(rank)
+    h = torch.randn(T, a.hidden, device="cuda", generator=g).to(torch.bfloat16)
+    bias = torch.randn(a.experts, device="cuda", generator=torch.Generator(device="cuda").manual_seed(0)) * 0.5
+    logits = torch.randn(T, a.experts, device="cuda", generator=g)
+    from .ops import core as C
+
+    w, ids = C.router_topk(logits, bias, a.moe_topk, "sigmoid", 2.5, True)
+    pctx.set_bounds([i * T for i in range(world + 1)])
+    shared = L.shared(h)
+
+    def step():
+        return pctx.moe(model, L, h, w, ids, shared)
+
+    ms = time_fn(step, iters=5, flush=False)
+    if world > 1:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    flops = 2 * T * a.moe_topk * 3 * a.hidden * a.inter      # routed experts (per rank's tokens)
+    bytes_nvlink = T * a.moe_topk * a.hidden * (1 + 2) * (world - 1) / max(world, 1)   # fp8 dispatch + bf16 combine
+    pk = peaks()
+    if rank == 0:
+        print(json.dumps({"bench": "moe_layer", "world": world, "comm": a.comm if world > 1 else "local",
+                          "tokens_per_rank": T, "experts": a.experts, "topk": a.moe_topk, "ms": round(ms, 3),
+                          "routed_tflops_per_gpu": round(flops / ms / 1e9, 1),
+                          "frac_of_fp8_peak(2x bf16 measured)": round(flops / ms / 1e9 / (2 * pk["bf16_tflops"]), 3),
+                          "nvlink_bytes_per_rank": int(bytes_nvlink), "peak_src": pk["src"]}))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["attn", "gemm", "mhc", "decode_attn"])
+    ap.add_argument("what", choices=["attn", "gemm", "mhc", "decode_attn", "moe"])
+    ap.add_argument("--experts", type=int, default=256)
+    ap.add_argument("--inter", type=int, default=2048)
+    ap.add_argument("--comm", default="fused", choices=["fused", "nccl"])
     ap.add_argument("--batch", type=int, default=4)
     ap.add_argument("--seq", type=int, default=8192)
     ap.add_argument("--heads", type=int, default=128)
     ap.add_argument("--dsa", action="store_true")
-    ap.add_argument("--topk", type=int, default=2048)
+    ap.add_argument("--topk", type=int, default=2048, help="DSA top-k")
+    ap.add_argument("--moe-topk", type=int, default=8, help="router top-k (moe)")
     ap.add_argument("--context", type=int, default=4096)
     ap.add_argument("--m", type=int, default=16384)
     ap.add_argument("--n", type=int, default=24576)
@@ -174,7 +241,8 @@ def main(argv=None):
     ap.add_argument("--hidden", type=int, default=7168)
     a = ap.parse_args(argv)
     sys.path.insert(0, ROOT)
-    {"attn": bench_attn, "gemm": bench_gemm, "mhc": bench_mhc, "decode_attn": bench_decode_attn}[a.what](a)
+    {"attn": bench_attn, "gemm": bench_gemm, "mhc": bench_mhc, "decode_attn": bench_decode_attn,
+     "moe": bench_moe}[a.what](a)
 
 
 if __name__ == "__main__":

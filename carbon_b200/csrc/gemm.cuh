@@ -329,6 +329,10 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
             amax = fmaxf(amax, fabsf(a));
           }
         }
+        // every TMEM read of this tile is done: hand the accumulator back before quantising and storing, so the
+        // MMAs of the next tile overlap this epilogue even with a single accumulator stage
+        tc_fence_before();
+        mbar_arrive(&tempty_bar[acc]);
         if (row_ok) {
           const uint32_t sb = ue8m0_for_amax(amax);
           const float inv = ue8m0_inv(sb);
@@ -351,8 +355,10 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
           *sf = uint8_t(sb);
         }
       }
-      tc_fence_before();
-      mbar_arrive(&tempty_bar[acc]);
+      if constexpr (EPI != EPI_SWIGLU_FP8) {
+        tc_fence_before();
+        mbar_arrive(&tempty_bar[acc]);
+      }
       ++iter;
     }
     if constexpr (EPI == EPI_BF16_SCATTER) __threadfence_system();   // peer stores performed before any barrier

@@ -144,6 +144,7 @@ class FusedCtx(DistCtx):
         b.local[:V].copy_(model.embed)
         model.embed = b.local[:V]
         self._embed = (b, per)
+        self.barrier()          # every shard is in place before any rank reads a peer's
 
     def embed(self, model, ids_all: torch.Tensor):
         self.adopt_embedding(model)
