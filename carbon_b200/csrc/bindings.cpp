@@ -276,6 +276,21 @@ void sparse_mla(torch::Tensor q, torch::Tensor kv, torch::Tensor idx, double sca
                     n_splits, po, pml, out.data_ptr(), nullptr, cur_stream()));
 }
 
+// decode-side DSA: q [T, H, 128] bf16, w [T, H] fp32, kc [S, 128] bf16, key_slots [T, L], n_keys [T] -> out [T, k]
+void indexer_topk(torch::Tensor q, torch::Tensor w, torch::Tensor kc, torch::Tensor key_slots, torch::Tensor n_keys,
+                  torch::Tensor out) {
+  CHECK_CUDA(q); CHECK_CONTIG(q); CHECK_CONTIG(kc); CHECK_CONTIG(key_slots); CHECK_CONTIG(out);
+  CHECK_DT(q, at::kBFloat16); CHECK_DT(kc, at::kBFloat16); CHECK_DT(w, at::kFloat);
+  const int T = q.size(0), L = key_slots.size(1);
+  auto logits = torch::empty({T, L}, q.options().dtype(at::kFloat));
+  c10::cuda::CUDAGuard g(q.device());
+  CK(cb::indexer_decode_logits(q.data_ptr(), w.contiguous().data_ptr<float>(), kc.data_ptr(),
+                               key_slots.data_ptr<int>(), n_keys.data_ptr<int>(), T, L, q.size(1), q.size(2),
+                               logits.data_ptr<float>(), cur_stream()));
+  CK(cb::topk_index(logits.data_ptr<float>(), key_slots.data_ptr<int>(), n_keys.data_ptr<int>(), T, L, out.size(1),
+                    out.data_ptr<int>(), cur_stream()));
+}
+
 }  // namespace
 
 void register_runtime(pybind11::module_& m);
@@ -306,4 +321,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("indexer_logits", &indexer_logits);
   m.def("topk_mask", &topk_mask);
   m.def("sparse_mla", &sparse_mla);
+  m.def("indexer_topk", &indexer_topk);
 }

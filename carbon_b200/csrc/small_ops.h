@@ -54,6 +54,10 @@ cudaError_t indexer_logits(const void* keys, int L, const void* q, int Tq, int H
                            int ldo, bool causal, int* status, int num_sms, cudaStream_t s);
 cudaError_t topk_mask(const float* logits, int ldo, int Tq, int k, uint32_t* mask, int mask_words, int row0,
                       cudaStream_t s);
+cudaError_t indexer_decode_logits(const void* q, const float* w, const void* kc, const int* key_slots,
+                                  const int* n_keys, int T, int Lmax, int H, int D, float* out, cudaStream_t s);
+cudaError_t topk_index(const float* logits, const int* key_slots, const int* n_keys, int T, int Lmax, int k,
+                       int* out, cudaStream_t s);
 
 // tcgen05 absorbed-MLA sparse attention over the latent cache (attn_decode.cu)
 cudaError_t sparse_mla(const void* q, int T, int H, const void* kv, int S, const int* idx, int K, float scale,

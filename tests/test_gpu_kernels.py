@@ -368,3 +368,22 @@ def test_bf16_gemm_split_k(M, N, K, splits):
     b = torch.randn(N, K).to(torch.bfloat16)
     out = bf16_gemm(a.to(DEV), b.to(DEV), out_dtype=torch.float32, k_splits=splits)
     assert rel_err(out, a.float() @ b.float().t()) < 1e-5
+
+
+@pytest.mark.parametrize("T,L,k", [(4, 300, 128), (3, 5000, 2048), (2, 100, 256)])
+def test_indexer_topk_decode(T, L, k):
+    from carbon_b200.ops.attention import indexer_topk
+
+    torch.manual_seed(12)
+    H, S = 64, 6000
+    q = torch.randn(T, H, 128).to(torch.bfloat16)
+    w = torch.randn(T, H) * 0.1
+    kc = torch.randn(S, 128).to(torch.bfloat16)
+    slots = torch.stack([torch.randperm(S)[:L] for _ in range(T)]).int()
+    n = torch.tensor([L - 7 * i for i in range(T)], dtype=torch.int32)
+    for i in range(T):
+        slots[i, int(n[i]):] = -1
+    got = indexer_topk(q.to(DEV), w.to(DEV), kc.to(DEV), slots.to(DEV), n.to(DEV), k).cpu()
+    ref = indexer_topk(q, w, kc, slots, n, k)
+    for i in range(T):
+        assert set(got[i][got[i] >= 0].tolist()) == set(ref[i][ref[i] >= 0].tolist()), i
