@@ -259,18 +259,24 @@ def main():
     dec_ms = max_over_ranks(sum(tp) / len(tp), world)
     tpot_p50 = max_over_ranks(statistics.median(tp), world)
 
-    launches = count_launches(eng, P, S)
-    if args.profile and rank == 0:
+    tables = []
+    if args.profile:                       # every rank runs the traced steps (they contain collectives)
         from carbon_b200.utils.trace import tracing
 
-        with tracing() as t:
-            prefill_step()
-        print("== prefill regions ==\n" + t.table(), file=sys.stderr, flush=True)
         eng.cuda_graphs = False
         with tracing() as t:
             eng.decode(reqs, next_ids())
-        eng.cuda_graphs = True
-        print("== decode regions (eager) ==\n" + t.table(), file=sys.stderr, flush=True)
+        eng.cuda_graphs = graphs
+        tables.append("== decode regions (eager) ==\n" + t.table())
+    for r in reqs:
+        eng.release(r)
+    launches = count_launches(eng, P, S)
+    if args.profile:
+        with tracing() as t:
+            prefill_step()
+        tables.append("== prefill regions ==\n" + t.table())
+        if rank == 0:
+            print("\n".join(tables), file=sys.stderr, flush=True)
     if world > 1:
         dist.barrier()
     if rank == 0:

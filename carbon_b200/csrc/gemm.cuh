@@ -295,12 +295,27 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
           const float* wq = p.idx_w + size_t(q_ok ? qi : 0) * p.idx_heads;
           float acc_l = 0.f;
 #pragma unroll 1
-          for (int c = 0; c < p.idx_heads; c += 16) {
-            uint32_t v[16];
-            tmem_ld_32x32b_x16(t_row + j * p.idx_heads + c, v);
+          for (int c = 0; c < p.idx_heads; c += 32) {
+            // two 16-column loads in flight, one wait (the head count is a multiple of 16)
+            uint32_t v[32];
+            uint32_t (&v0)[16] = *reinterpret_cast<uint32_t(*)[16]>(&v[0]);
+            uint32_t (&v1)[16] = *reinterpret_cast<uint32_t(*)[16]>(&v[16]);
+            const bool two = c + 16 < p.idx_heads;
+            tmem_ld_32x32b_x16(t_row + j * p.idx_heads + c, v0);
+            if (two) tmem_ld_32x32b_x16(t_row + j * p.idx_heads + c + 16, v1);
+            const float4* w4 = reinterpret_cast<const float4*>(wq + c);
+            float wv[32];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const float4 x = (i < 4 || two) ? w4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+              wv[4 * i] = x.x; wv[4 * i + 1] = x.y; wv[4 * i + 2] = x.z; wv[4 * i + 3] = x.w;
+            }
             tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 16; ++i) acc_l += wq[c + i] * fmaxf(__uint_as_float(v[i]), 0.f);
+            for (int i = 0; i < 16; ++i) acc_l += wv[i] * fmaxf(__uint_as_float(v[i]), 0.f);
+            if (two)
+#pragma unroll
+              for (int i = 16; i < 32; ++i) acc_l += wv[i] * fmaxf(__uint_as_float(v[i]), 0.f);
           }
           if (row_ok && q_ok) {
             float* o = reinterpret_cast<float*>(p.out) + size_t(qi) * p.ldo + key;

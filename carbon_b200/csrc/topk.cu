@@ -66,9 +66,17 @@ __global__ void topk_mask_kernel(const float* __restrict__ logits, int ldo, int 
     for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
     __syncthreads();
     const uint32_t prefix = s_prefix;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-      const uint32_t u = vals[i];
-      if ((u & known) == prefix) atomicAdd(&hist[(u >> shift) & 255], 1);
+    for (int i0 = 0; i0 < n; i0 += blockDim.x) {
+      // warp-aggregated histogram update: lanes hitting the same bin add once (values of one row share most of
+      // their high bits, so plain atomics would serialise on a few bins)
+      const int i = i0 + threadIdx.x;
+      int bin = -1;
+      if (i < n) {
+        const uint32_t u = vals[i];
+        if ((u & known) == prefix) bin = int((u >> shift) & 255);
+      }
+      const unsigned grp = __match_any_sync(0xffffffffu, bin);
+      if (bin >= 0 && (threadIdx.x & 31) == __ffs(grp) - 1) atomicAdd(&hist[bin], __popc(grp));
     }
     __syncthreads();
     if (threadIdx.x == 0) {
@@ -197,9 +205,17 @@ __global__ void topk_index_kernel(const float* __restrict__ logits, const int* _
     for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
     __syncthreads();
     const uint32_t prefix = s_prefix;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) {
-      const uint32_t u = vals[i];
-      if ((u & known) == prefix) atomicAdd(&hist[(u >> shift) & 255], 1);
+    for (int i0 = 0; i0 < n; i0 += blockDim.x) {
+      // warp-aggregated histogram update: lanes hitting the same bin add once (values of one row share most of
+      // their high bits, so plain atomics would serialise on a few bins)
+      const int i = i0 + threadIdx.x;
+      int bin = -1;
+      if (i < n) {
+        const uint32_t u = vals[i];
+        if ((u & known) == prefix) bin = int((u >> shift) & 255);
+      }
+      const unsigned grp = __match_any_sync(0xffffffffu, bin);
+      if (bin >= 0 && (threadIdx.x & 31) == __ffs(grp) - 1) atomicAdd(&hist[bin], __popc(grp));
     }
     __syncthreads();
     if (threadIdx.x == 0) {

@@ -122,6 +122,23 @@ class Layer:
     pass
 
 
+class Pending:
+    """A tensor being produced on a side stream; ``get()`` joins the side stream into the current one."""
+
+    def __init__(self, tensor: torch.Tensor, stream):
+        self.tensor, self.stream = tensor, stream
+
+    def get(self) -> torch.Tensor:
+        cur = torch.cuda.current_stream()
+        cur.wait_stream(self.stream)
+        self.tensor.record_stream(cur)
+        return self.tensor
+
+
+def resolve(x):
+    return x.get() if isinstance(x, Pending) else x
+
+
 class DeepseekModel:
     def __init__(self, cfg: ModelConfig, source: WeightSource, device="cpu", fp8: bool = True,
                  pctx=None):
@@ -133,6 +150,7 @@ class DeepseekModel:
         self.pctx = pctx if pctx is not None else ParallelCtx.single()
         self.fp8 = fp8
         self.trace = None          # set to a list to record (name, tensor) at sublayer boundaries (debugging)
+        self._side = None          # side stream of the shared expert
         cfg.validate()
         tp, ep = self.pctx.tp, self.pctx.ep
         self.H_local = cfg.n_heads // tp
@@ -390,8 +408,17 @@ class DeepseekModel:
             w, ids = C.router_topk(logits, L.gate_b, cfg.n_activated_experts, cfg.score_func, cfg.route_scale,
                                    cfg.norm_topk_prob)
         self._tr(f"{i}.router_ids", ids)
-        with region("moe.shared"):
-            shared = L.shared(h, xq=hq) if L.shared is not None else None
+        shared = None
+        if L.shared is not None:
+            if self.on_gpu:
+                # shared expert on a side stream, overlapping the routed experts; the combine joins it
+                if self._side is None:
+                    self._side = torch.cuda.Stream()
+                self._side.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.stream(self._side), region("moe.shared"):
+                    shared = Pending(L.shared(h, xq=hq), self._side)
+            else:
+                shared = L.shared(h, xq=hq)
         return self.pctx.moe(self, L, h, w, ids, shared)
 
     def moe_local(self, L, h, w, ids, shared):
@@ -419,7 +446,7 @@ class DeepseekModel:
             y = fp8_gemm(act, act_sf, L.e_w2, m_block_expert=lay.m_block_expert, num_m_blocks=lay.num_blocks,
                          n_per_group=cfg.hidden_size)
         with region("moe.combine"):
-            return C.moe_combine(y, w, lay.slot_pos, shared, T)
+            return C.moe_combine(y, w, lay.slot_pos, resolve(shared), T)
 
     # ------------------------------------------------------------------------------------------------------------------
     # whole model

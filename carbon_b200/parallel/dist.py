@@ -167,7 +167,9 @@ class DistCtx(ParallelCtx):
         contrib[order] = back.float()
         out = (contrib.view(T, k, -1) * w.float()[..., None]).sum(1)
         if shared is not None:
-            out = out + shared.float()
+            from ..models.deepseek import resolve
+
+            out = out + resolve(shared).float()
         return out.to(h.dtype)
 
     def lm_head(self, model, y: torch.Tensor) -> torch.Tensor:

@@ -183,25 +183,32 @@ class FusedCtx(DistCtx):
         El, E = model.E_local, cfg.n_routed_experts
         m = self._moe_bufs(model, T)
         ids = ids.to(torch.int32).contiguous()
-        pair_rank = torch.empty(T * k, dtype=torch.int32, device=h.device)
-        e.moe_count(ids.view(-1), E, self.rank, m["cnt"].peers, pair_rank)
-        self.barrier()
-        e.moe_owner_layout(m["cnt"].local, self.world, El, m["off"].local, m["mbe"], m["nb"])
-        self.barrier()
-        pos = torch.empty(T, k, dtype=torch.int32, device=h.device)
-        e.moe_dispatch(h.contiguous(), ids, El, self.rank, pair_rank, m["recv"].peers, m["sf"].peers,
-                       m["off"].peers, m["cap"], pos, self.status)
-        self.barrier()
+        from ..models.deepseek import resolve
+        from ..utils.trace import region
+
+        with region("moe.dispatch"):
+            pair_rank = torch.empty(T * k, dtype=torch.int32, device=h.device)
+            e.moe_count(ids.view(-1), E, self.rank, m["cnt"].peers, pair_rank)
+            self.barrier()
+            e.moe_owner_layout(m["cnt"].local, self.world, El, m["off"].local, m["mbe"], m["nb"])
+            self.barrier()
+            pos = torch.empty(T, k, dtype=torch.int32, device=h.device)
+            e.moe_dispatch(h.contiguous(), ids, El, self.rank, pair_rank, m["recv"].peers, m["sf"].peers,
+                           m["off"].peers, m["cap"], pos, self.status)
+            self.barrier()
         # owner: grouped GEMMs over the expert-sorted received rows, in place in the heap
         I2 = 2 * cfg.moe_intermediate
-        act, act_sf = fp8_gemm_swiglu(m["recv"].local, m["sf"].local, L.e_w13, cfg.swiglu_limit, m["mbe"], m["nb"],
-                                      I2)
-        fp8_gemm(act, act_sf, L.e_w2, out=m["y"].local, m_block_expert=m["mbe"], num_m_blocks=m["nb"],
-                 n_per_group=cfg.hidden_size)
-        self.barrier()
-        out = torch.empty(T, cfg.hidden_size, dtype=torch.bfloat16, device=h.device)
-        e.moe_combine_pull(m["y"].peers, ids, pos, w.float().contiguous(), El, shared, out)
-        self.barrier()     # peers may not reuse `y` until every rank has pulled its rows
+        with region("moe.gemm_up"):
+            act, act_sf = fp8_gemm_swiglu(m["recv"].local, m["sf"].local, L.e_w13, cfg.swiglu_limit, m["mbe"],
+                                          m["nb"], I2)
+        with region("moe.gemm_down"):
+            fp8_gemm(act, act_sf, L.e_w2, out=m["y"].local, m_block_expert=m["mbe"], num_m_blocks=m["nb"],
+                     n_per_group=cfg.hidden_size)
+        with region("moe.combine"):
+            self.barrier()
+            out = torch.empty(T, cfg.hidden_size, dtype=torch.bfloat16, device=h.device)
+            e.moe_combine_pull(m["y"].peers, ids, pos, w.float().contiguous(), El, resolve(shared), out)
+            self.barrier()     # peers may not reuse `y` until every rank has pulled its rows
         return out
 
     def lm_head(self, model, y: torch.Tensor) -> torch.Tensor:
