@@ -97,10 +97,10 @@ def bench_gemm(a):
     W = quantize_weight(torch.randn(a.n, a.k, device="cuda") * 0.02)
     q, sf = quant_act(x)
     out = torch.empty(a.m, a.n, dtype=torch.bfloat16, device="cuda")
-    ms = time_fn(lambda: fp8_gemm(q, sf, W, out=out))
+    ms = time_fn(lambda: fp8_gemm(q, sf, W, out=out, pair=a.pair))
     flops = 2 * a.m * a.n * a.k
     pk = peaks()
-    print(json.dumps({"bench": "fp8_gemm", "m": a.m, "n": a.n, "k": a.k, "ms": round(ms, 3),
+    print(json.dumps({"bench": "fp8_gemm", "m": a.m, "n": a.n, "k": a.k, "pair": a.pair, "ms": round(ms, 3),
                       "tflops": round(flops / ms / 1e9, 1),
                       "frac_of_bf16_peak_x2": round(flops / ms / 1e9 / (2 * pk["bf16_tflops"]), 3),
                       "peak_src": pk["src"]}))
@@ -239,6 +239,7 @@ def main(argv=None):
     ap.add_argument("--k", type=int, default=7168)
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--hidden", type=int, default=7168)
+    ap.add_argument("--pair", type=int, default=-1, help="gemm: -1 auto, 1 CTA-pair 256x256 tiles, 0 128x128 tiles")
     a = ap.parse_args(argv)
     sys.path.insert(0, ROOT)
     {"attn": bench_attn, "gemm": bench_gemm, "mhc": bench_mhc, "decode_attn": bench_decode_attn,

@@ -170,6 +170,7 @@ class KernelFlags:
     cuda_graphs: bool = True        # capture decode steps
     fp8_gemm: bool = True           # block-scaled fp8 GEMMs (else bf16)
     sparse_attention: bool = True   # DSA top-k attention when the model has an indexer
+    moe_align: int = 0              # expert segment padding: 0 automatic, 128, or 256 (CTA-pair GEMM tiles)
 
     @classmethod
     def from_env(cls) -> "KernelFlags":

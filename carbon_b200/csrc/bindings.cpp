@@ -84,13 +84,14 @@ void router_topk(torch::Tensor logits, c10::optional<torch::Tensor> bias, int64_
 }
 
 void moe_layout(torch::Tensor ids, int64_t E, torch::Tensor slot_pos, torch::Tensor row_src,
-                torch::Tensor m_block_expert, torch::Tensor num_blocks, c10::optional<torch::Tensor> counts) {
+                torch::Tensor m_block_expert, torch::Tensor num_blocks, c10::optional<torch::Tensor> counts,
+                int64_t align) {
   CHECK_CUDA(ids); CHECK_DT(ids, at::kInt); CHECK_CONTIG(ids);
   TORCH_CHECK(row_src.numel() >= m_block_expert.numel() * 128);
   c10::cuda::CUDAGuard g(ids.device());
   CK(cb::moe_layout(ids.data_ptr<int>(), ids.size(0), ids.size(1), E, m_block_expert.numel(),
                     slot_pos.data_ptr<int>(), row_src.data_ptr<int>(), m_block_expert.data_ptr<int>(),
-                    num_blocks.data_ptr<int>(), ptr_or_null<int>(counts), cur_stream()));
+                    num_blocks.data_ptr<int>(), ptr_or_null<int>(counts), cur_stream(), int(align)));
 }
 
 void moe_combine(torch::Tensor Y, torch::Tensor w, torch::Tensor slot_pos, c10::optional<torch::Tensor> add,
@@ -170,7 +171,8 @@ void silu_mul(torch::Tensor gu, double limit, torch::Tensor out) {
 // ---------------------------------------------------------------------------------------------------------------
 void gemm_fp8(torch::Tensor A, torch::Tensor sfa, torch::Tensor B, torch::Tensor sfb, torch::Tensor out, int64_t epi,
               c10::optional<torch::Tensor> out_sf, double swiglu_limit, c10::optional<torch::Tensor> m_block_expert,
-              c10::optional<torch::Tensor> num_m_blocks, int64_t N_per_group, c10::optional<torch::Tensor> status) {
+              c10::optional<torch::Tensor> num_m_blocks, int64_t N_per_group, c10::optional<torch::Tensor> status,
+              int64_t pair) {
   CHECK_CUDA(A); CHECK_DT(A, at::kFloat8_e4m3fn); CHECK_DT(B, at::kFloat8_e4m3fn); CHECK_CONTIG(A); CHECK_CONTIG(B);
   CHECK_DT(sfa, at::kInt); CHECK_DT(sfb, at::kInt);
   const int M = A.size(0), K = A.size(1);
@@ -195,7 +197,7 @@ void gemm_fp8(torch::Tensor A, torch::Tensor sfa, torch::Tensor B, torch::Tensor
                   reinterpret_cast<uint32_t*>(sfb.data_ptr()), M, N, K, Nb, out.data_ptr(), out.stride(0), epi,
                   ptr_or_null<uint32_t>(out_sf), float(swiglu_limit), ptr_or_null<const int>(m_block_expert),
                   ptr_or_null<const int>(num_m_blocks), grouped ? m_block_expert->numel() : 0,
-                  ptr_or_null<int>(status), num_sms(), cur_stream()));
+                  ptr_or_null<int>(status), num_sms(), cur_stream(), int(pair)));
 }
 
 void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor out, int64_t epi,

@@ -19,7 +19,7 @@ cudaError_t reduce_slots(const void* slots, int world, int slot_rows, int n, int
 cudaError_t moe_count(const int* ids, int Tk, int E, int world, int my_rank, const uint64_t* cnt_ptrs,
                       int* pair_rank, cudaStream_t s);
 cudaError_t moe_owner_layout(const int* cnt, int world, int El, int max_blocks, int* src_off, int* m_block_expert,
-                             int* num_blocks, cudaStream_t s);
+                             int* num_blocks, cudaStream_t s, int align);
 cudaError_t moe_dispatch(const void* x, int T, int D, const int* ids, int k, int El, int my_rank,
                          const int* pair_rank, const uint64_t* recv_ptrs, const uint64_t* sf_ptrs,
                          const uint64_t* off_ptrs, int cap, int* pos_out, int* status, cudaStream_t s);
@@ -123,9 +123,9 @@ void moe_count(torch::Tensor ids, int64_t E, int64_t my_rank, torch::Tensor cnt_
                     pair_rank.data_ptr<int>(), stream()));
 }
 void moe_owner_layout(torch::Tensor cnt, int64_t world, int64_t El, torch::Tensor src_off,
-                      torch::Tensor m_block_expert, torch::Tensor num_blocks) {
+                      torch::Tensor m_block_expert, torch::Tensor num_blocks, int64_t align) {
   CKP(cb::moe_owner_layout(cnt.data_ptr<int>(), world, El, m_block_expert.numel(), src_off.data_ptr<int>(),
-                           m_block_expert.data_ptr<int>(), num_blocks.data_ptr<int>(), stream()));
+                           m_block_expert.data_ptr<int>(), num_blocks.data_ptr<int>(), stream(), int(align)));
 }
 void moe_dispatch(torch::Tensor x, torch::Tensor ids, int64_t El, int64_t my_rank, torch::Tensor pair_rank,
                   torch::Tensor recv_ptrs, torch::Tensor sf_ptrs, torch::Tensor off_ptrs, int64_t cap,

@@ -2,6 +2,7 @@
 #include <cudaTypedefs.h>
 #include <mutex>
 #include "gemm.cuh"
+#include "gemm_pair.cuh"
 #include "small_ops.h"
 
 namespace cb {
@@ -34,6 +35,54 @@ bool make_tmap_2d(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, int e
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   (void)elem_bytes;
   return r == CUDA_SUCCESS;
+}
+
+// Scale-factor tiles as a 2-D tensor of uint32: [rows = K/512 * row_blocks][128 words], one box = `box_rows` tiles.
+static bool make_tmap_sf(CUtensorMap* m, const uint32_t* sf, uint64_t rows, uint32_t box_rows) {
+  auto fn = tmap_encode_fn();
+  if (!fn || (reinterpret_cast<uintptr_t>(sf) & 15)) return false;
+  cuuint64_t dims[2] = {128, rows};
+  cuuint64_t strides[1] = {512};
+  cuuint32_t box[2] = {128, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(sf), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Launch of the pair-tile GEMM: clusters of PAIR CTAs, one persistent cluster per co-resident slot.
+template <int KIND, int EPI, int PAIR, int ST>
+static cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tsa,
+                               const CUtensorMap& tsb, const GemmParams& p, int max_units, int num_sms,
+                               cudaStream_t s) {
+  using C = PairCfg<KIND, PAIR>;
+  constexpr int smem = gemm_pair_smem_bytes<KIND, PAIR, ST>();
+  auto kern = gemm_pair_kernel<KIND, EPI, PAIR, ST>;
+  static int resident = 0;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = PAIR; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (!resident) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    int n = 0;
+    cfg.gridDim = dim3((num_sms / PAIR) * PAIR);
+    if (PAIR > 1 && cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0)
+      resident = n < num_sms / PAIR ? n : num_sms / PAIR;
+    else
+      resident = num_sms / PAIR;
+    cudaGetLastError();
+  }
+  const int units = max_units < resident ? max_units : resident;
+  if (units <= 0) return cudaSuccess;
+  cfg.gridDim = dim3(units * PAIR);
+  return cudaLaunchKernelEx(&cfg, kern, ta, tb, tsa, tsb, p);
 }
 
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int M, int N, int ldo,
@@ -74,9 +123,33 @@ static cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const Ge
 cudaError_t gemm_fp8(const void* A, const void* B, const uint32_t* sfa, const uint32_t* sfb, int M, int N, int K,
                      int Nb, void* out, int ldo, int epi, uint32_t* out_sf, float swiglu_limit,
                      const int* m_block_expert, const int* num_m_blocks_dev, int max_m_blocks, int* status,
-                     int num_sms, cudaStream_t s) {
+                     int num_sms, cudaStream_t s, int pair) {
   if (M <= 0 || N <= 0) return cudaSuccess;
   if (K % 128 || N % 16) return cudaErrorInvalidValue;
+  // pair-tile kernel: dense prefill-sized GEMMs, and grouped GEMMs whose expert segments are 256-row aligned
+  // (the caller says so with pair = 1); the 128-row kernel keeps decode-sized and fp32-output GEMMs
+  const bool use_pair = epi != GEMM_OUT_F32 && (pair == 1 || (pair < 0 && !m_block_expert && M >= 512));
+  if (use_pair) {
+    if (N % 256 && (m_block_expert || epi == GEMM_OUT_SWIGLU_FP8)) return cudaErrorInvalidValue;
+    if (m_block_expert && (max_m_blocks & 1)) return cudaErrorInvalidValue;
+    CUtensorMap ta, tb, tsa, tsb;
+    if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, K, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, Nb, K, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_tmap_sf(&tsa, sfa, uint64_t(ceil_div(K, 512)) * ceil_div(M, 128), 1) ||
+        !make_tmap_sf(&tsb, sfb, uint64_t(ceil_div(K, 512)) * ceil_div(Nb, 128), 2))
+      return cudaErrorInvalidValue;
+    GemmParams p{};
+    p.M = M; p.N = N; p.K = K;
+    p.sfa = sfa; p.sfb = sfb;
+    p.sfa_row_blocks = ceil_div(M, 128);
+    p.sfb_row_blocks = ceil_div(Nb, 128);
+    p.out = out; p.ldo = ldo; p.out_sf = out_sf; p.swiglu_limit = swiglu_limit;
+    p.m_block_expert = m_block_expert; p.num_m_blocks_dev = num_m_blocks_dev; p.status = status;
+    const int units = (m_block_expert ? max_m_blocks / 2 : ceil_div(M, 256)) * ceil_div(N, 256);
+    if (epi == GEMM_OUT_SWIGLU_FP8)
+      return launch_pair<KIND_MXF8, EPI_SWIGLU_FP8, 2, 6>(ta, tb, tsa, tsb, p, units, num_sms, s);
+    return launch_pair<KIND_MXF8, EPI_BF16, 2, 6>(ta, tb, tsa, tsb, p, units, num_sms, s);
+  }
   const int BN = (epi == GEMM_OUT_SWIGLU_FP8) ? 256 : 128;
   if (m_block_expert && (N % BN)) return cudaErrorInvalidValue;
   if (BN == 256 && (Nb % 256)) return cudaErrorInvalidValue;  // SF tiles of a 256-row B block must exist
@@ -152,6 +225,15 @@ cudaError_t gemm_fp8_scatter(const void* A, const void* B, const uint32_t* sfa, 
   p.ldo = N; p.status = status;
   p.scatter_ptrs = scatter_ptrs; p.scatter_bounds = bounds; p.scatter_world = world; p.scatter_rank = my_rank;
   p.scatter_rows = slot_rows;
+  if (M >= 512) {
+    CUtensorMap tb2, tsa, tsb;
+    if (!make_tmap_2d(&tb2, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, K, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_tmap_sf(&tsa, sfa, uint64_t(ceil_div(K, 512)) * ceil_div(M, 128), 1) ||
+        !make_tmap_sf(&tsb, sfb, uint64_t(ceil_div(K, 512)) * ceil_div(N, 128), 2))
+      return cudaErrorInvalidValue;
+    return launch_pair<KIND_MXF8, EPI_BF16_SCATTER, 2, 6>(ta, tb2, tsa, tsb, p, ceil_div(M, 256) * ceil_div(N, 256),
+                                                        num_sms, s);
+  }
   return launch<KIND_MXF8, EPI_BF16_SCATTER, 128, 6, 2>(ta, tb, p, ceil_div(M, 128) * ceil_div(N, 128), num_sms, s);
 }
 
@@ -161,18 +243,19 @@ cudaError_t indexer_logits(const void* keys, int L, const void* q, int Tq, int H
   if (L <= 0 || Tq <= 0) return cudaSuccess;
   constexpr int BN = 256;
   if (Di % 64 || BN % H || H % 16) return cudaErrorInvalidValue;
+  if ((BN / H) % 2) return cudaErrorInvalidValue;          // two epilogue halves split a tile's queries
   CUtensorMap ta, tb;
   if (!make_tmap_2d(&ta, keys, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Di, L, uint64_t(Di) * 2, 64, 128,
                     CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_tmap_2d(&tb, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Di, uint64_t(Tq) * H, uint64_t(Di) * 2, 64, BN,
+      !make_tmap_2d(&tb, q, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Di, uint64_t(Tq) * H, uint64_t(Di) * 2, 64, 64,
                     CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
   GemmParams p{};
   p.M = L; p.N = Tq * H; p.K = Di;
   p.out = out; p.ldo = ldo; p.status = status;
   p.idx_w = w; p.idx_heads = H; p.causal = causal ? 1 : 0;
-  const int max_tiles = ceil_div(L, 128) * ceil_div(Tq * H, BN);
-  return launch<KIND_BF16, EPI_INDEXER, 256, 4, 2>(ta, tb, p, max_tiles, num_sms, s);
+  const int units = ceil_div(L, 256) * ceil_div(Tq * H, BN);
+  return launch_pair<KIND_BF16, EPI_INDEXER, 2, 6>(ta, tb, ta, tb, p, units, num_sms, s);
 }
 
 }  // namespace cb

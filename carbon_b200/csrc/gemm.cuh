@@ -268,7 +268,9 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
                   reinterpret_cast<uint4*>(o)[j] = w;
                 }
               } else {
-                for (int j = 0; j < 32 && col0 + j < p.N; ++j) o[j] = __float2bfloat16_rn(__uint_as_float(v[j]));
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (col0 + j < p.N) o[j] = __float2bfloat16_rn(__uint_as_float(v[j]));
               }
             } else {
               float* o = reinterpret_cast<float*>(p.out) + size_t(row) * p.ldo + col0;
@@ -281,7 +283,9 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
                 for (int j = 0; j < 8; ++j)
                   reinterpret_cast<uint4*>(o)[j] = make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
               } else {
-                for (int j = 0; j < 32 && col0 + j < p.N; ++j) o[j] = __uint_as_float(v[j]);
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (col0 + j < p.N) o[j] = __uint_as_float(v[j]);
               }
             }
           }

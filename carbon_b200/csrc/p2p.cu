@@ -170,7 +170,7 @@ cudaError_t moe_count(const int* ids, int Tk, int E, int world, int my_rank, con
 // every 128-row block, and the row offset of each source inside each expert segment. cnt: [world][El].
 __global__ void moe_owner_layout_kernel(const int* __restrict__ cnt, int world, int El, int max_blocks,
                                         int* __restrict__ src_off, int* __restrict__ m_block_expert,
-                                        int* __restrict__ num_blocks) {
+                                        int* __restrict__ num_blocks, int align) {
   if (threadIdx.x != 0) return;
   int acc = 0, b = 0;
   for (int e = 0; e < El; ++e) {
@@ -179,7 +179,7 @@ __global__ void moe_owner_layout_kernel(const int* __restrict__ cnt, int world, 
       src_off[sr * El + e] = acc + n;
       n += cnt[sr * El + e];
     }
-    const int nb = (n + 127) / 128;
+    const int nb = (n + align - 1) / align * (align / 128);   // 128-row blocks, segment padded to `align` rows
     for (int j = 0; j < nb && b < max_blocks; ++j) m_block_expert[b++] = e;
     acc += nb * 128;
   }
@@ -188,8 +188,9 @@ __global__ void moe_owner_layout_kernel(const int* __restrict__ cnt, int world, 
 }
 
 cudaError_t moe_owner_layout(const int* cnt, int world, int El, int max_blocks, int* src_off, int* m_block_expert,
-                             int* num_blocks, cudaStream_t s) {
-  moe_owner_layout_kernel<<<1, 32, 0, s>>>(cnt, world, El, max_blocks, src_off, m_block_expert, num_blocks);
+                             int* num_blocks, cudaStream_t s, int align) {
+  if (align != 128 && align != 256) return cudaErrorInvalidValue;
+  moe_owner_layout_kernel<<<1, 32, 0, s>>>(cnt, world, El, max_blocks, src_off, m_block_expert, num_blocks, align);
   return cudaGetLastError();
 }
 

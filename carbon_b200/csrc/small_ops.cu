@@ -304,7 +304,7 @@ cudaError_t router_topk(const float* logits, const float* bias, int T, int E, in
 __global__ void moe_layout_kernel(const int* __restrict__ ids, int Tk, int k, int E, int max_blocks,
                                   int* __restrict__ slot_pos, int* __restrict__ row_src,
                                   int* __restrict__ m_block_expert, int* __restrict__ num_blocks,
-                                  int* __restrict__ counts_out) {
+                                  int* __restrict__ counts_out, int align) {
   __shared__ int cnt[1024];
   __shared__ int start[1024];
   __shared__ int fill[1024];
@@ -317,11 +317,11 @@ __global__ void moe_layout_kernel(const int* __restrict__ ids, int Tk, int k, in
   __syncthreads();
   if (threadIdx.x == 0) {
     int acc = 0;
-    for (int e = 0; e < E; ++e) { start[e] = acc; acc += (cnt[e] + 127) & ~127; }
+    for (int e = 0; e < E; ++e) { start[e] = acc; acc += (cnt[e] + align - 1) / align * align; }
     const int nb = acc >> 7;
     num_blocks[0] = nb;
     for (int e = 0, b = 0; e < E; ++e) {
-      const int nbe = (cnt[e] + 127) >> 7;
+      const int nbe = (cnt[e] + align - 1) / align * (align >> 7);
       for (int j = 0; j < nbe && b < max_blocks; ++j) m_block_expert[b++] = e;
     }
     for (int b = nb; b < max_blocks; ++b) m_block_expert[b] = -1;
@@ -342,10 +342,10 @@ __global__ void moe_layout_kernel(const int* __restrict__ ids, int Tk, int k, in
   }
 }
 cudaError_t moe_layout(const int* ids, int T, int k, int E, int max_blocks, int* slot_pos, int* row_src,
-                       int* m_block_expert, int* num_blocks, int* counts, cudaStream_t s) {
-  if (E > 1024) return cudaErrorInvalidValue;
+                       int* m_block_expert, int* num_blocks, int* counts, cudaStream_t s, int align) {
+  if (E > 1024 || (align != 128 && align != 256)) return cudaErrorInvalidValue;
   moe_layout_kernel<<<1, 1024, 0, s>>>(ids, T * k, k, E, max_blocks, slot_pos, row_src, m_block_expert, num_blocks,
-                                       counts);
+                                       counts, align);
   return cudaGetLastError();
 }
 

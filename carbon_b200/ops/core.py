@@ -68,14 +68,35 @@ def router_topk(logits: torch.Tensor, bias: Optional[torch.Tensor], k: int, scor
     return w, ids
 
 
-class MoeLayout:
-    """Expert-sorted row layout of one MoE call (every expert segment padded to 128 rows)."""
+_ALIGN_FLAG = None
 
-    def __init__(self, ids: torch.Tensor, n_experts: int, max_blocks: Optional[int] = None):
+
+def moe_align(rows: int, n_experts: int) -> int:
+    """Row alignment of expert segments: 256 (CTA-pair GEMM tiles) once experts average enough rows that the extra
+    padding costs less than the pair tiles save, else 128.  ``CARBON_MOE_ALIGN`` (KernelFlags.moe_align) pins it."""
+    global _ALIGN_FLAG
+    if _ALIGN_FLAG is None:
+        from ..config import KernelFlags
+
+        _ALIGN_FLAG = KernelFlags.from_env().moe_align
+    if _ALIGN_FLAG in (128, 256):
+        return _ALIGN_FLAG
+    return 256 if rows >= 768 * n_experts else 128
+
+
+class MoeLayout:
+    """Expert-sorted row layout of one MoE call: every expert segment padded to `align` rows (128 or 256), blocks
+    of 128 rows tagged with their expert."""
+
+    def __init__(self, ids: torch.Tensor, n_experts: int, max_blocks: Optional[int] = None, align: int = 0):
         T, k = ids.shape
         dev = ids.device
+        if align == 0:
+            align = moe_align(T * k, n_experts)
+        self.align = align
         if max_blocks is None:
-            max_blocks = (T * k + 127) // 128 + n_experts
+            max_blocks = (T * k + 127) // 128 + n_experts * (align // 128)
+            max_blocks += max_blocks & 1
         self.T, self.k, self.E, self.max_blocks = T, k, n_experts, max_blocks
         self.slot_pos = torch.empty(T, k, dtype=torch.int32, device=dev)
         self.row_src = torch.empty(max_blocks * 128, dtype=torch.int32, device=dev)
@@ -84,7 +105,7 @@ class MoeLayout:
         self.counts = torch.empty(n_experts, dtype=torch.int32, device=dev)
         if ids.is_cuda:
             ext().moe_layout(ids.contiguous(), n_experts, self.slot_pos, self.row_src, self.m_block_expert,
-                             self.num_blocks, self.counts)
+                             self.num_blocks, self.counts, align)
         else:
             self._cpu(ids)
 
@@ -97,7 +118,7 @@ class MoeLayout:
         mbe = []
         for e in range(E):
             start[e] = acc
-            nb = (int(counts[e]) + 127) // 128
+            nb = (int(counts[e]) + self.align - 1) // self.align * (self.align // 128)
             mbe += [e] * nb
             acc += nb * 128
         self.num_blocks[0] = len(mbe)
@@ -116,6 +137,11 @@ class MoeLayout:
     @property
     def rows(self) -> int:
         return self.max_blocks * 128
+
+    @property
+    def pair(self) -> int:
+        """GEMM tile mode for this layout (1 = CTA-pair tiles, 0 = 128-row tiles)."""
+        return 1 if self.align == 256 else 0
 
 
 def moe_combine(Y: torch.Tensor, w: torch.Tensor, slot_pos: torch.Tensor, add: Optional[torch.Tensor],

@@ -160,9 +160,14 @@ class FusedCtx(DistCtx):
     def _moe_bufs(self, model, T_l: int):
         cfg = model.cfg
         D, El, k = cfg.hidden_size, model.E_local, cfg.n_activated_experts
-        cap = int(self.max_local * k * self.moe_capacity) + El * 128
-        cap = (cap + 127) // 128 * 128
-        if self._moe is None:
+        from ..ops.core import moe_align
+
+        # expert segments of the owner's buffer are padded to 256 rows (CTA-pair GEMM tiles) when experts average
+        # enough rows; the choice depends only on static sizes, so every rank makes the same one
+        align = moe_align(self.max_local * k * self.world, El * self.world)
+        cap = int(self.max_local * k * self.moe_capacity) + El * align
+        cap = (cap + 255) // 256 * 256
+        if self._moe is None or self._moe["align"] != align:
             h = self.heap
             self._moe = {
                 "cnt": h.alloc((self.world, El), torch.int32),
@@ -173,6 +178,7 @@ class FusedCtx(DistCtx):
                 "cap": cap,
                 "mbe": torch.empty(cap // 128, dtype=torch.int32, device=self.device),
                 "nb": torch.empty(1, dtype=torch.int32, device=self.device),
+                "align": align,
             }
         return self._moe
 
@@ -190,7 +196,7 @@ class FusedCtx(DistCtx):
             pair_rank = torch.empty(T * k, dtype=torch.int32, device=h.device)
             e.moe_count(ids.view(-1), E, self.rank, m["cnt"].peers, pair_rank)
             self.barrier()
-            e.moe_owner_layout(m["cnt"].local, self.world, El, m["off"].local, m["mbe"], m["nb"])
+            e.moe_owner_layout(m["cnt"].local, self.world, El, m["off"].local, m["mbe"], m["nb"], m["align"])
             self.barrier()
             pos = torch.empty(T, k, dtype=torch.int32, device=h.device)
             e.moe_dispatch(h.contiguous(), ids, El, self.rank, pair_rank, m["recv"].peers, m["sf"].peers,
@@ -200,10 +206,10 @@ class FusedCtx(DistCtx):
         I2 = 2 * cfg.moe_intermediate
         with region("moe.gemm_up"):
             act, act_sf = fp8_gemm_swiglu(m["recv"].local, m["sf"].local, L.e_w13, cfg.swiglu_limit, m["mbe"],
-                                          m["nb"], I2)
+                                          m["nb"], I2, pair=int(m["align"] == 256))
         with region("moe.gemm_down"):
             fp8_gemm(act, act_sf, L.e_w2, out=m["y"].local, m_block_expert=m["mbe"], num_m_blocks=m["nb"],
-                     n_per_group=cfg.hidden_size)
+                     n_per_group=cfg.hidden_size, pair=int(m["align"] == 256))
         with region("moe.combine"):
             self.barrier()
             out = torch.empty(T, cfg.hidden_size, dtype=torch.bfloat16, device=h.device)

@@ -1,0 +1,171 @@
+"""CTA-pair (cta_group::2) 256x256-tile GEMM: numerics against the fp32 oracle and against the 128-row kernel.
+
+Covers dense bf16 output (ragged M and N, short and long K, several tiles per persistent CTA pair so both
+accumulator stages and their shared TMEM columns are exercised), expert-grouped SwiGLU + down projection on a
+256-row-aligned layout, the o_proj scatter epilogue, and the DSA indexer epilogue.
+"""
+import pytest
+import torch
+
+from carbon_b200.ref import ops as R
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def _ext():
+    from carbon_b200.ops._ext import ext
+
+    return ext()
+
+
+def rel_err(a, b):
+    a, b = a.float().cpu(), b.float().cpu()
+    return ((a - b).norm() / (b.norm() + 1e-12)).item()
+
+
+def _weight(N, K, seed, scale=0.02):
+    from carbon_b200.ops.quant import Fp8Weight
+
+    g = torch.Generator().manual_seed(seed)
+    W = Fp8Weight.from_float(torch.randn(N, K, generator=g) * scale)
+    return W, Fp8Weight(W.q.to(DEV), W.sf.to(DEV), W.scale.to(DEV))
+
+
+@pytest.mark.parametrize("M,N,K", [(512, 256, 512), (1000, 1536, 2048), (777, 576, 7168), (4096, 4096, 1024),
+                                   (1024, 512, 128), (2048, 7168, 1536)])
+def test_pair_gemm_dense_matches_oracle_and_single_cta(M, N, K):
+    from carbon_b200.ops.gemm import fp8_gemm
+    from carbon_b200.ops.quant import quant_act
+
+    torch.manual_seed(11)
+    x = torch.randn(M, K).to(torch.bfloat16)
+    W, Wd = _weight(N, K, 12)
+    q, sf = quant_act(x.to(DEV))
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out_pair = fp8_gemm(q, sf, Wd, pair=1, status=status)
+    out_single = fp8_gemm(q, sf, Wd, pair=0)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    q_ref, s_ref = R.quant_fp8_rows(x.float())
+    ref = R.fp8_gemm(q_ref, s_ref, W.q, W.scale)
+    assert rel_err(out_pair, ref) < 5e-3, rel_err(out_pair, ref)
+    # same products in the same K order: the two kernels agree to bf16 rounding
+    assert rel_err(out_pair, out_single) < 1e-3
+
+
+def test_pair_gemm_repeated_launches_are_deterministic():
+    from carbon_b200.ops.gemm import fp8_gemm
+    from carbon_b200.ops.quant import quant_act
+
+    x = torch.randn(3000, 2048, device=DEV).to(torch.bfloat16)
+    _, Wd = _weight(3072, 2048, 13)
+    q, sf = quant_act(x)
+    a = fp8_gemm(q, sf, Wd, pair=1)
+    for _ in range(3):
+        b = fp8_gemm(q, sf, Wd, pair=1)
+        assert torch.equal(a, b)
+
+
+def _grouped(T, E, k, seed, align):
+    from carbon_b200.ops.core import MoeLayout
+
+    g = torch.Generator().manual_seed(seed)
+    ids = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(torch.int32)
+    return ids, MoeLayout(ids.to(DEV), E, align=align)
+
+
+def test_layout_align_256_blocks():
+    T, E, k = 700, 6, 2
+    ids, lay = _grouped(T, E, k, 21, 256)
+    torch.cuda.synchronize()
+    counts = torch.bincount(ids.view(-1).long(), minlength=E)
+    nb = int(lay.num_blocks.cpu())
+    assert nb == int(((counts + 255) // 256).sum()) * 2
+    mbe = lay.m_block_expert.cpu()
+    assert all(int(mbe[2 * i]) == int(mbe[2 * i + 1]) for i in range(nb // 2))
+    slot = lay.slot_pos.cpu()
+    for t in range(T):
+        for j in range(k):
+            assert int(mbe[int(slot[t, j]) // 128]) == int(ids[t, j])
+
+
+def test_pair_grouped_swiglu_and_down_projection():
+    from carbon_b200.ops.gemm import fp8_gemm, fp8_gemm_swiglu, interleave_gate_up
+    from carbon_b200.ops.quant import Fp8Weight, pack_sf, quant_act, unpack_sf
+
+    T, E, k, K, I, D = 900, 4, 2, 512, 256, 512
+    ids, lay = _grouped(T, E, k, 22, 256)
+    assert lay.pair == 1
+    g = torch.Generator().manual_seed(23)
+    x = torch.randn(T, K, generator=g).to(torch.bfloat16)
+    w1 = torch.randn(E, I, K, generator=g) * 0.05
+    w3 = torch.randn(E, I, K, generator=g) * 0.05
+    w2 = torch.randn(E, D, I, generator=g) * 0.05
+    W13 = [Fp8Weight.from_float(interleave_gate_up(w1[e], w3[e])) for e in range(E)]
+    W2 = [Fp8Weight.from_float(w2[e]) for e in range(E)]
+
+    def stack(Ws, rows):
+        return Fp8Weight(torch.cat([W.q for W in Ws]).to(DEV),
+                         pack_sf(torch.cat([W.scale.repeat_interleave(128, 0)[:rows] for W in Ws])).to(DEV), None)
+
+    q, sf = quant_act(x.to(DEV), src_rows=lay.row_src)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    act, act_sf = fp8_gemm_swiglu(q, sf, stack(W13, 2 * I), 0.0, lay.m_block_expert, lay.num_blocks, 2 * I,
+                                  status=status, pair=1)
+    y = fp8_gemm(act, act_sf, stack(W2, D), m_block_expert=lay.m_block_expert, num_m_blocks=lay.num_blocks,
+                 n_per_group=D, status=status, pair=1)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    rows = lay.rows
+    act_d = act.cpu().float() * unpack_sf(act_sf.cpu(), rows, I).repeat_interleave(128, 1)
+    q_ref, s_ref = R.quant_fp8_rows(x.float())
+    xd = R.dequant_fp8_rows(q_ref, s_ref)
+    slot = lay.slot_pos.cpu()
+    y = y.cpu()
+    for t in range(0, T, 7):
+        for j in range(k):
+            e = int(ids[t, j])
+            gu = (xd[t] @ W13[e].dequant().t()).view(-1, 2, 128)
+            ref_act = R.swiglu(gu[:, 0].reshape(-1), gu[:, 1].reshape(-1))
+            p = int(slot[t, j])
+            assert rel_err(act_d[p], ref_act) < 0.04
+            ref_y = act_d[p] @ W2[e].dequant().t()
+            assert rel_err(y[p], ref_y) < 1e-2
+
+
+def test_pair_scatter_epilogue_single_rank():
+    """o_proj GEMM -> row scatter with one rank: the rows land in slot 0 of this rank's own buffer."""
+    from carbon_b200.ops.quant import quant_act
+
+    M, N, K = 1100, 1024, 2048
+    x = torch.randn(M, K, device=DEV).to(torch.bfloat16)
+    W, Wd = _weight(N, K, 31)
+    q, sf = quant_act(x)
+    buf = torch.zeros(M, N, dtype=torch.bfloat16, device=DEV)
+    ptrs = torch.tensor([buf.data_ptr()], dtype=torch.int64, device=DEV)
+    bounds = torch.tensor([0, M], dtype=torch.int32, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    _ext().gemm_fp8_scatter(q, sf, Wd.q, Wd.sf, ptrs, bounds, 0, M, status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    from carbon_b200.ops.gemm import fp8_gemm
+
+    ref = fp8_gemm(q, sf, Wd, pair=0)
+    assert rel_err(buf, ref) < 1e-3
+
+
+@pytest.mark.parametrize("n,H", [(300, 64), (1100, 64), (700, 32), (530, 16), (260, 128)])
+def test_pair_indexer_logits(n, H):
+    torch.manual_seed(6)
+    q = torch.randn(n, H, 128).to(torch.bfloat16)
+    k = torch.randn(n, 128).to(torch.bfloat16)
+    w = torch.randn(n, H)
+    ldo = (n + 3) // 4 * 4
+    out = torch.full((n, ldo), float("nan"), device=DEV)
+    _ext().indexer_logits(k.to(DEV), q.to(DEV), w.to(DEV), out, True)
+    ref = R.indexer_logits(q.float(), k.float(), w)
+    causal = torch.ones(n, n, dtype=torch.bool).tril_()
+    got = out[:, :n].cpu()
+    assert rel_err(got[causal], ref[causal]) < 1e-5
