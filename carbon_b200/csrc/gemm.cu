@@ -55,7 +55,7 @@ template <int KIND, int EPI, int PAIR, int ST>
 static cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tsa,
                                const CUtensorMap& tsb, const GemmParams& p, int max_units, int num_sms,
                                cudaStream_t s) {
-  using C = PairCfg<KIND, PAIR>;
+  using C = PairCfg<KIND, PAIR, EPI>;
   constexpr int smem = gemm_pair_smem_bytes<KIND, PAIR, ST>();
   auto kern = gemm_pair_kernel<KIND, EPI, PAIR, ST>;
   static int resident = 0;

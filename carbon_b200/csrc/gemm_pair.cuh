@@ -26,7 +26,7 @@
 
 namespace cb {
 
-template <int KIND, int PAIR>
+template <int KIND, int PAIR, int EPI = EPI_BF16>
 struct PairCfg {
   static constexpr int BN = 256;                       // tile N (each CTA stages BN/PAIR rows of B)
   static constexpr int BM = 128 * PAIR;                // tile M (each CTA: 128 rows of A, 128 accumulator lanes)
@@ -42,24 +42,26 @@ struct PairCfg {
   static constexpr uint32_t kAcc0 = kScaled ? 32 : 0;
   static constexpr uint32_t kAcc1 = 512 - BN;
   static constexpr int kOvl = int(kAcc0) + BN - int(kAcc1);   // columns shared by the two stages (32 or 0)
-  static constexpr int kEpiWarps = 8;
+  // the indexer epilogue is latency bound (one short reduction per query): four warps per lane quadrant
+  static constexpr int kEpiWarps = EPI == EPI_INDEXER ? 16 : 8;
+  static constexpr int kParts = kEpiWarps / 4;         // epilogue warps per TMEM lane quadrant
   static constexpr int kThreads = 128 + 32 * kEpiWarps;
 };
 
 template <int KIND, int PAIR, int STAGES>
 constexpr int gemm_pair_smem_bytes() {
-  using C = PairCfg<KIND, PAIR>;
+  using C = PairCfg<KIND, PAIR, EPI_BF16>;
   return 1024 + STAGES * (C::TILE_A + C::TILE_B + C::SFA_BYTES + C::SFB_BYTES) + 8 * (2 * STAGES + 8) + 16 +
          2 * 2 * 128 * 4;
 }
 
 template <int KIND, int EPI, int PAIR, int STAGES>
-__global__ void __launch_bounds__(PairCfg<KIND, PAIR>::kThreads, 1)
+__global__ void __launch_bounds__(PairCfg<KIND, PAIR, EPI>::kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                      const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
                      const GemmParams p) {
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 1000
-  using C = PairCfg<KIND, PAIR>;
+  using C = PairCfg<KIND, PAIR, EPI>;
   constexpr int BN = C::BN, BM = C::BM, BK = C::BK;
   constexpr bool kScaled = C::kScaled;
   constexpr int kMmaPerStage = BK / C::UMMA_K;
@@ -275,7 +277,7 @@ __global__ void __launch_bounds__(PairCfg<KIND, PAIR>::kThreads, 1)
       }
     }
   } else if (warp >= 4) {
-    // ================= epilogue: 8 warps, quadrant q = warp % 4, column half h =================
+    // ================= epilogue: quadrant q = warp % 4, part h (column half, or query slot for the indexer) ======
     const uint32_t q = warp & 3;
     const uint32_t h = (warp - 4) >> 2;
     const int row_in_cta = int(q * 32 + lane);
@@ -398,19 +400,20 @@ __global__ void __launch_bounds__(PairCfg<KIND, PAIR>::kThreads, 1)
           }
         }
       } else {
-        // DSA indexer: A rows are keys, tile columns are qpt queries x H heads; half h owns queries
-        // [h*qpt/2, (h+1)*qpt/2).  logits[q, key] = sum_h w[q,h] * relu(acc[key, q*H + h]); -inf where key > q.
+        // DSA indexer: A rows are keys, tile columns are qpt queries x H heads; part h of the quadrant owns queries
+        // h, h + kParts, ...  logits[q, key] = sum_h w[q,h] * relu(acc[key, q*H + h]); -inf where key > q.
         const int H = p.idx_heads;
-        const int qpt = BN / H, qh = qpt / 2;
+        const int qpt = BN / H;
         const int key = row;
 #pragma unroll 1
-        for (int jq = int(h) * qh; jq < int(h + 1) * qh; ++jq) {
+        for (int jq = int(h); jq < qpt; jq += C::kParts) {
           const int qi = nb * qpt + jq;
           const bool q_ok = qi * H < p.N;
           const float* wq = p.idx_w + size_t(q_ok ? qi : 0) * H;
-          float acc_l = 0.f;
+          float acc4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
           for (int c = 0; c < H; c += 32) {
+            // two 16-column loads in flight, one wait (the head count is a multiple of 16)
             uint32_t v[32];
             uint32_t (&v0)[16] = *reinterpret_cast<uint32_t(*)[16]>(&v[0]);
             uint32_t (&v1)[16] = *reinterpret_cast<uint32_t(*)[16]>(&v[16]);
@@ -421,19 +424,19 @@ __global__ void __launch_bounds__(PairCfg<KIND, PAIR>::kThreads, 1)
             float wv[32];
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-              const float4 x = (i < 4 || two) ? w4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+              const float4 x = (i < 4 || two) ? __ldg(w4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
               wv[4 * i] = x.x; wv[4 * i + 1] = x.y; wv[4 * i + 2] = x.z; wv[4 * i + 3] = x.w;
             }
             tmem_ld_wait();
 #pragma unroll
-            for (int i = 0; i < 16; ++i) acc_l = fmaf(wv[i], fmaxf(__uint_as_float(v[i]), 0.f), acc_l);
+            for (int i = 0; i < 16; ++i) acc4[i & 3] = fmaf(wv[i], fmaxf(__uint_as_float(v[i]), 0.f), acc4[i & 3]);
             if (two)
 #pragma unroll
-              for (int i = 16; i < 32; ++i) acc_l = fmaf(wv[i], fmaxf(__uint_as_float(v[i]), 0.f), acc_l);
+              for (int i = 16; i < 32; ++i) acc4[i & 3] = fmaf(wv[i], fmaxf(__uint_as_float(v[i]), 0.f), acc4[i & 3]);
           }
           if (row_ok && q_ok) {
             float* o = reinterpret_cast<float*>(p.out) + size_t(qi) * p.ldo + key;
-            *o = (p.causal && key > qi) ? -INFINITY : acc_l;
+            *o = (p.causal && key > qi) ? -INFINITY : (acc4[0] + acc4[1]) + (acc4[2] + acc4[3]);
           }
         }
         release(&tempty_full[s]);

@@ -244,8 +244,10 @@ CB_DEVICE uint32_t mapa_shared(uint32_t cta_addr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(cta_addr), "r"(rank));
   return r;
 }
+// Arrive on an mbarrier of any CTA of the cluster (default .release.cta: hands off tcgen05 work ordered by
+// tcgen05.fence::before_thread_sync without waiting for this thread's outstanding global stores).
 CB_DEVICE void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 // TMA tile load into this CTA's shared memory whose completion is counted on an mbarrier of either CTA of the
 // pair (`bar_cluster_addr`, from mapa).  Plain unicast load.

@@ -40,6 +40,23 @@ CB_DEVICE int block_incl_scan(int v, int* sw) {
   return r;
 }
 
+// All threads of the block: given the 256-bin histogram of this radix digit (over the keys that still match
+// `prefix`), find the digit d such that the keys in bins above d number < rem <= those in bins >= d; record the
+// extended prefix and how many keys of digit d remain to be taken.  A block scan over the bins in descending order
+// replaces a 256-step serial walk.
+CB_DEVICE void select_digit(const int* hist, int* sw, uint32_t* s_prefix, int* s_remaining, uint32_t prefix,
+                            int shift) {
+  const int t = threadIdx.x;
+  const int rem = *s_remaining;                  // read by every thread before the scan's barriers
+  const int c = t < 256 ? hist[255 - t] : 0;
+  const int incl = block_incl_scan(c, sw);
+  if (t < 256 && incl >= rem && incl - c < rem) {
+    *s_remaining = rem - (incl - c);
+    *s_prefix = prefix | (uint32_t(255 - t) << shift);
+  }
+  __syncthreads();
+}
+
 __global__ void topk_mask_kernel(const float* __restrict__ logits, int ldo, int Tq, int k, uint32_t* __restrict__ mask,
                                  int mask_words, int row0) {
   extern __shared__ uint32_t vals[];
@@ -79,17 +96,8 @@ __global__ void topk_mask_kernel(const float* __restrict__ logits, int ldo, int 
       if (bin >= 0 && (threadIdx.x & 31) == __ffs(grp) - 1) atomicAdd(&hist[bin], __popc(grp));
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-      int rem = s_remaining, c = 0, d = 255;
-      for (; d > 0; --d) {
-        if (c + hist[d] >= rem) break;
-        c += hist[d];
-      }
-      s_remaining = rem - c;
-      s_prefix = prefix | (uint32_t(d) << shift);
-    }
+    select_digit(hist, sw, &s_prefix, &s_remaining, prefix, shift);
     known |= 255u << shift;
-    __syncthreads();
   }
   const uint32_t thr = s_prefix;
   const int take_eq = s_remaining;               // how many keys equal to thr are selected (lowest indices first)
@@ -218,17 +226,8 @@ __global__ void topk_index_kernel(const float* __restrict__ logits, const int* _
       if (bin >= 0 && (threadIdx.x & 31) == __ffs(grp) - 1) atomicAdd(&hist[bin], __popc(grp));
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-      int rem = s_remaining, c = 0, d = 255;
-      for (; d > 0; --d) {
-        if (c + hist[d] >= rem) break;
-        c += hist[d];
-      }
-      s_remaining = rem - c;
-      s_prefix = prefix | (uint32_t(d) << shift);
-    }
+    select_digit(hist, sw, &s_prefix, &s_remaining, prefix, shift);
     known |= 255u << shift;
-    __syncthreads();
   }
   const uint32_t thr = s_prefix;
   const int take_eq = s_remaining;

@@ -81,7 +81,7 @@ def moe_align(rows: int, n_experts: int) -> int:
         _ALIGN_FLAG = KernelFlags.from_env().moe_align
     if _ALIGN_FLAG in (128, 256):
         return _ALIGN_FLAG
-    return 256 if rows >= 768 * n_experts else 128
+    return 256 if rows >= 384 * n_experts else 128
 
 
 class MoeLayout:
