@@ -329,6 +329,285 @@ static bool make_tmap_3d(CUtensorMap* m, const void* ptr, uint64_t d0, uint64_t 
 
 }  // namespace fa
 
+// ---------------------------------------------------------------------------------------------------------------
+// Two-tile variant: one CTA runs two 128-row Q tiles of the same (sequence, head) against each K/V tile.
+//
+//   warp 0  TMA: Q0/Q1 once, then K(j) (3 chunks: k_nope 0-63, 64-127, shared RoPE key) and V(j) (2 chunks) into a
+//           FIFO ring of NCH 16 KB chunks, so V(j+1) streams in as soon as K(j) has been consumed
+//   warp 1  MMA, issue order  QK0(0) QK1(0) | PV0(0) QK0(1) PV1(0) QK1(1) | PV0(1) QK0(2) ...: while the softmax of
+//           one tile runs, the tensor core works on the other tile
+//   warp 2  TMEM allocator
+//   warps 4-7 / 8-11  softmax of tile 0 / tile 1: one query row per thread (all 128 scores in registers, no
+//           cross-warp reduction), lazy O rescale, P written back into TMEM over S as bf16 and read by the PV MMA
+//           straight from TMEM (A operand in tensor memory); O/l written out at the end
+// TMEM: tile t uses columns [256t, 256t+128) for S (P in its first 64 columns) and [256t+128, 256t+256) for O.
+// ---------------------------------------------------------------------------------------------------------------
+namespace fa2 {
+
+constexpr int BM = 128, BN = 128, DQK = 192, DV = 128;
+constexpr int ATOM = 128 * 128;                 // one [128 rows x 128 B] swizzled box = one ring chunk
+constexpr int Q_BYTES = 3 * ATOM;               // 48 KB per Q tile
+constexpr int NCH = 8;                          // ring chunks (K = 3, V = 2 per KV tile)
+constexpr int CH_PER_KV = 5;
+constexpr int SMEM = 1024 + 2 * Q_BYTES + NCH * ATOM + 512;
+constexpr float kRescaleThresh = 8.0f;
+
+__global__ void __launch_bounds__(384, 1) attn_prefill2_kernel(const __grid_constant__ CUtensorMap tm_q,
+                                                               const __grid_constant__ CUtensorMap tm_kv,
+                                                               const __grid_constant__ CUtensorMap tm_kpe,
+                                                               const fa::Params p) {
+#if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 1000
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;                          // [2 tiles][3 atoms]
+  uint8_t* sR = sQ + 2 * Q_BYTES;              // ring [NCH][ATOM]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sR + NCH * ATOM);
+  uint64_t* q_full = bars;                     // 1
+  uint64_t* r_full = bars + 1;                 // [NCH]
+  uint64_t* r_empty = bars + 1 + NCH;          // [NCH]
+  uint64_t* s_full = bars + 1 + 2 * NCH;       // [2]
+  uint64_t* p_full = bars + 3 + 2 * NCH;       // [2]
+  uint64_t* o_done = bars + 5 + 2 * NCH;       // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7 + 2 * NCH);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int4 tile = p.tiles[blockIdx.x];
+  const int seq_start = tile.x, seq_len = tile.y, q0 = tile.z;
+  const int h = blockIdx.y;
+  int n_kt_t[2];
+  for (int t = 0; t < 2; ++t) {
+    const int qt0 = q0 + BM * t;
+    n_kt_t[t] = qt0 < seq_len ? (min(qt0 + BM, seq_len) + BN - 1) / BN : 0;
+  }
+  const int n_kt = max(n_kt_t[0], n_kt_t[1]);
+  const bool two = n_kt_t[1] > 0;
+
+  const uint32_t warp = warp_id(), lane = lane_id();
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < NCH; ++i) { mbar_init(&r_full[i], 1); mbar_init(&r_empty[i], 1); }
+    for (int t = 0; t < 2; ++t) { mbar_init(&s_full[t], 1); mbar_init(&p_full[t], 128); mbar_init(&o_done[t], 1); }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto fail = [&](int code) { if (p.status) atomicCAS(p.status, 0, code); *abort_flag = 1; };
+  auto chunk = [&](int idx) -> uint8_t* { return sR + (idx % NCH) * ATOM; };
+
+  if (warp == 0) {
+    // ================= TMA producer =================
+    if (elect_one()) {
+      tma_prefetch_desc(&tm_q); tma_prefetch_desc(&tm_kv); tma_prefetch_desc(&tm_kpe);
+      mbar_arrive_expect_tx(q_full, (two ? 2 : 1) * Q_BYTES);
+      for (int t = 0; t < (two ? 2 : 1); ++t)
+        for (int a = 0; a < 3; ++a)
+          tma_load_3d(sQ + t * Q_BYTES + a * ATOM, &tm_q, q_full, a * 64, h, seq_start + q0 + BM * t);
+      for (int idx = 0; idx < n_kt * CH_PER_KV && !*abort_flag; ++idx) {
+        const int slot = idx % NCH, use = idx / NCH;
+        if (!mbar_wait(&r_empty[slot], (use & 1) ^ 1)) { fail(kErrTimeoutEmpty); break; }
+        mbar_arrive_expect_tx(&r_full[slot], ATOM);
+        const int j = idx / CH_PER_KV, c = idx % CH_PER_KV;
+        const int row = seq_start + j * BN;
+        if (c < 2) tma_load_3d(sR + slot * ATOM, &tm_kv, &r_full[slot], c * 64, h, row);          // k_nope
+        else if (c == 2) tma_load_2d(sR + slot * ATOM, &tm_kpe, &r_full[slot], 0, row);            // RoPE key
+        else tma_load_3d(sR + slot * ATOM, &tm_kv, &r_full[slot], 128 + (c - 3) * 64, h, row);    // v
+      }
+    }
+  } else if (warp == 1) {
+    // ================= MMA issuer =================
+    if (elect_one()) {
+      const uint32_t id_qk = idesc_bf16(BM, BN);
+      const uint32_t id_pv = fa::idesc_bf16_bmn(BM, 64);
+      bool ok = mbar_wait(q_full, 0);
+      if (!ok) fail(kErrTimeoutFull);
+      auto wait_chunks = [&](int first, int n) -> bool {
+        for (int i = 0; i < n; ++i) {
+          const int idx = first + i;
+          if (!mbar_wait(&r_full[idx % NCH], (idx / NCH) & 1)) { fail(kErrTimeoutFull); return false; }
+        }
+        tc_fence_after();
+        return true;
+      };
+      auto release_chunks = [&](int first, int n) {
+        for (int i = 0; i < n; ++i) mma_commit(&r_empty[(first + i) % NCH]);
+      };
+      auto qk = [&](int t, int j) {
+        const int kc = j * CH_PER_KV;
+#pragma unroll
+        for (int k = 0; k < DQK / 16; ++k) {
+          const int a = k >> 2, off = (k & 3) * 32;
+          mma_f16_ss(tmem + 256 * t, smem_desc_sw128(sQ + t * Q_BYTES + a * ATOM + off),
+                     smem_desc_sw128(chunk(kc + a) + off), id_qk, k > 0);
+        }
+        mma_commit(&s_full[t]);
+      };
+      auto pv = [&](int t, int j) {
+        const int vc = j * CH_PER_KV + 3;
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint8_t* v = chunk(vc + half);
+#pragma unroll
+          for (int k = 0; k < BN / 16; ++k) {
+            // A = P from TMEM: 16 keys = 8 columns of packed bf16; B = V chunk (MN-major, 64 dv wide)
+            mma_f16_ts(tmem + 256 * t + 128 + 64 * half, tmem + 256 * t + 8 * k,
+                       fa::desc_mn_sw128(v + k * 16 * 128, ATOM, 1024), id_pv, (j > 0 || k > 0) ? 1u : 0u);
+          }
+        }
+        mma_commit(&o_done[t]);
+      };
+      if (ok && n_kt > 0) {
+        ok = wait_chunks(0, 3);
+        if (ok) {
+          qk(0, 0);
+          if (two) qk(1, 0);
+          release_chunks(0, 3);
+        }
+      }
+      for (int j = 0; ok && j < n_kt && !*abort_flag; ++j) {
+        bool v_ready = false, k_ready = false;
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (j >= n_kt_t[t]) continue;
+          if (!mbar_wait(&p_full[t], j & 1)) { fail(kErrTimeoutTmem); ok = false; break; }
+          tc_fence_after();
+          if (!v_ready) { ok = wait_chunks(j * CH_PER_KV + 3, 2); v_ready = true; if (!ok) break; }
+          pv(t, j);
+          if (j + 1 < n_kt_t[t]) {
+            if (!k_ready) { ok = wait_chunks((j + 1) * CH_PER_KV, 3); k_ready = true; if (!ok) break; }
+            qk(t, j + 1);
+          }
+        }
+        if (!ok) break;
+        release_chunks(j * CH_PER_KV + 3, 2);
+        if (j + 1 < n_kt) release_chunks((j + 1) * CH_PER_KV, 3);
+      }
+    }
+  } else if (warp >= 4) {
+    // ================= softmax: tile t = (warp-4)/4, TMEM lane quadrant q, one query row per thread =================
+    const int t = int(warp - 4) >> 2;
+    const uint32_t q = warp & 3;
+    const int row = int(q * 32 + lane);
+    const int qt0 = q0 + BM * t;
+    const int qi = qt0 + row;
+    const int tok = seq_start + qi;
+    const uint32_t t_lane = tmem + ((q * 32) << 16) + 256 * t;
+    const int nkt = n_kt_t[t];
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nkt; ++j) {
+      if (!mbar_wait(&s_full[t], j & 1)) { fail(kErrTimeoutTmem); ok = false; break; }
+      tc_fence_after();
+      float sv[128];
+      {
+        uint32_t (&r0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[0]);
+        uint32_t (&r1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[32]);
+        uint32_t (&r2)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[64]);
+        uint32_t (&r3)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[96]);
+        tmem_ld_32x32b_x32(t_lane + 0, r0);
+        tmem_ld_32x32b_x32(t_lane + 32, r1);
+        tmem_ld_32x32b_x32(t_lane + 64, r2);
+        tmem_ld_32x32b_x32(t_lane + 96, r3);
+        tmem_ld_wait();
+      }
+      const int k0 = j * BN;
+      float mt = -INFINITY;
+      const bool dense_tile = (p.mask == nullptr) && (k0 + BN - 1 <= qt0);
+      if (dense_tile) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) mt = fmaxf(mt, sv[i]);
+        mt *= p.scale_log2;
+      } else {
+        uint32_t mw[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
+        if (p.mask && qi < seq_len) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int wi = (k0 >> 5) + c;
+            mw[c] = wi < p.mask_words ? p.mask[size_t(tok) * p.mask_words + wi] : 0u;
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 128; ++i) {
+          const bool allowed = (k0 + i <= qi) && ((mw[i >> 5] >> (i & 31)) & 1u);
+          sv[i] = allowed ? sv[i] : -INFINITY;
+          mt = fmaxf(mt, sv[i]);
+        }
+        mt = mt == -INFINITY ? mt : mt * p.scale_log2;
+      }
+      const bool need = (j > 0) && (mt > m_used + kRescaleThresh);
+      const float m_new = (need || j == 0) ? fmaxf(m_used, mt) : m_used;
+      const float m_ref = m_new == -INFINITY ? 0.f : m_new;
+      float alpha = 1.f;
+      if (need && m_used != -INFINITY) alpha = fa::fast_exp2(m_used - m_ref);
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // O still holds the sums of earlier tiles at the old max: wait for the last PV, then rescale in TMEM
+        if (!mbar_wait(&o_done[t], (j - 1) & 1)) { fail(kErrTimeoutTmem); ok = false; break; }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 128; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_lane + 128 + c, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st_32x32b_x32(t_lane + 128 + c, r);
+        }
+      }
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float a = fa::fast_exp2(fmaf(sv[32 * c + 2 * i], p.scale_log2, -m_ref));
+          const float b = fa::fast_exp2(fmaf(sv[32 * c + 2 * i + 1], p.scale_log2, -m_ref));
+          rs += a + b;
+          pk[i] = pack_bf16x2(a, b);
+        }
+        tmem_st_32x32b_x16(t_lane + 16 * c, pk);     // P over the first 64 columns of S
+      }
+      l = l * alpha + rs;
+      m_used = m_new;
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&p_full[t]);
+    }
+    if (ok && nkt > 0) {
+      if (!mbar_wait(&o_done[t], (nkt - 1) & 1)) { fail(kErrTimeoutTmem); ok = false; }
+    }
+    if (ok && nkt > 0) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* o = p.out + (size_t(tok) * p.H + h) * DV;
+#pragma unroll 1
+      for (int c = 0; c < DV; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_lane + 128 + c, r);
+        tmem_ld_wait();
+        if (qi < seq_len) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]) * inv, __uint_as_float(r[8 * v + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]) * inv, __uint_as_float(r[8 * v + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * inv, __uint_as_float(r[8 * v + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * inv, __uint_as_float(r[8 * v + 7]) * inv);
+            reinterpret_cast<uint4*>(o + c)[v] = w;
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 2) { tc_fence_after(); tmem_dealloc(tmem, 512); }
+#endif
+}
+
+}  // namespace fa2
+
+
 // Host: q [T,H,192], kvb [T,H,256] (k_nope | v), kpe [T,64] bf16 contiguous; tiles [n_tiles] int4; out [T,H,128].
 cudaError_t attn_prefill(const void* q, const void* kvb, const void* kpe, int T, int H, const int* tiles,
                          int n_tiles, const uint32_t* mask, int mask_words, float scale, void* out, int* status,
@@ -391,6 +670,38 @@ cudaError_t attn_prefill(const void* q, const void* kvb, const void* kpe, int T,
   p.status = status;
   dim3 grid(n_tiles, H);
   attn_prefill_kernel<<<grid, 384, SMEM, s>>>(tq, tkv, tkpe, p);
+  return cudaGetLastError();
+}
+
+// Two-tile kernel: tiles are (seq_start, seq_len, q0, 0) with q0 a multiple of 256.
+cudaError_t attn_prefill2(const void* q, const void* kvb, const void* kpe, int T, int H, const int* tiles,
+                          int n_tiles, const uint32_t* mask, int mask_words, float scale, void* out, int* status,
+                          cudaStream_t s) {
+  using namespace fa;
+  if (n_tiles == 0) return cudaSuccess;
+  CUtensorMap tq, tkv, tkpe;
+  if (!make_tmap_3d(&tq, q, DQK, H, T, DQK * 2, uint64_t(H) * DQK * 2, 64, 1, BM) ||
+      !make_tmap_3d(&tkv, kvb, 256, H, T, 256 * 2, uint64_t(H) * 256 * 2, 64, 1, BN) ||
+      !make_tmap_2d(&tkpe, kpe, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64, T, 64 * 2, 64, BN,
+                    CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(fa2::attn_prefill2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         fa2::SMEM);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  Params p;
+  p.tiles = reinterpret_cast<const int4*>(tiles);
+  p.mask = mask;
+  p.mask_words = mask_words;
+  p.H = H;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.status = status;
+  dim3 grid(n_tiles, H);
+  fa2::attn_prefill2_kernel<<<grid, 384, fa2::SMEM, s>>>(tq, tkv, tkpe, p);
   return cudaGetLastError();
 }
 

@@ -225,7 +225,7 @@ void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor out, int64_t epi,
 // q [T, H, 192], kvb [T, H, 256] (k_nope | v), kpe [T, 64] -> out [T, H, 128]
 void attn_prefill(torch::Tensor q, torch::Tensor kvb, torch::Tensor kpe, torch::Tensor tiles,
                   c10::optional<torch::Tensor> mask, double scale, torch::Tensor out,
-                  c10::optional<torch::Tensor> status) {
+                  c10::optional<torch::Tensor> status, int64_t version) {
   CHECK_CUDA(q); CHECK_DT(q, at::kBFloat16); CHECK_DT(kvb, at::kBFloat16); CHECK_DT(kpe, at::kBFloat16);
   CHECK_CONTIG(q); CHECK_CONTIG(kvb); CHECK_CONTIG(kpe); CHECK_CONTIG(out); CHECK_DT(tiles, at::kInt);
   TORCH_CHECK(q.size(2) == 192 && kvb.size(2) == 256 && kpe.size(-1) == 64, "attn_prefill: MLA dims 192/128");
@@ -235,9 +235,10 @@ void attn_prefill(torch::Tensor q, torch::Tensor kvb, torch::Tensor kpe, torch::
   int words = 0;
   if (mask.has_value()) { CHECK_DT((*mask), at::kInt); TORCH_CHECK(mask->size(0) == T); words = mask->size(1); }
   c10::cuda::CUDAGuard g(q.device());
-  CK(cb::attn_prefill(q.data_ptr(), kvb.data_ptr(), kpe.data_ptr(), T, H, tiles.data_ptr<int>(), tiles.size(0),
-                      ptr_or_null<const uint32_t>(mask), words, float(scale), out.data_ptr(),
-                      ptr_or_null<int>(status), cur_stream()));
+  auto fn = version == 2 ? cb::attn_prefill2 : cb::attn_prefill;
+  CK(fn(q.data_ptr(), kvb.data_ptr(), kpe.data_ptr(), T, H, tiles.data_ptr<int>(), tiles.size(0),
+        ptr_or_null<const uint32_t>(mask), words, float(scale), out.data_ptr(), ptr_or_null<int>(status),
+        cur_stream()));
 }
 
 // keys [L, Di] bf16, q [Tq, H, Di] bf16, w [Tq, H] fp32 -> logits [Tq, ldo] fp32

@@ -280,14 +280,17 @@ def test_mhc_kernels():
 # ----------------------------------------------------------------------------------------------------------------------
 # attention
 # ----------------------------------------------------------------------------------------------------------------------
-@pytest.mark.parametrize("lens,masked", [([128], False), ([300, 77, 5], False), ([513], True), ([200, 260], True)])
-def test_attn_prefill(lens, masked):
+@pytest.mark.parametrize("version", [1, 2])
+@pytest.mark.parametrize("lens,masked,qscale", [([128], False, 1.0), ([300, 77, 5], False, 1.0), ([513], True, 1.0),
+                                                ([200, 260], True, 1.0), ([1000, 700], False, 4.0),
+                                                ([1300], True, 3.0), ([256, 384, 129], False, 1.0)])
+def test_attn_prefill(lens, masked, qscale, version):
     from carbon_b200.ops.attention import prefill_attention
 
     torch.manual_seed(5)
     H = 4
     T = sum(lens)
-    q = torch.randn(T, H, 192).to(torch.bfloat16)
+    q = (torch.randn(T, H, 192) * qscale).to(torch.bfloat16)     # qscale > 1: row maxima keep growing (rescales)
     k = torch.randn(T, H, 192).to(torch.bfloat16)
     k[..., 128:] = torch.randn(T, 1, 64).to(torch.bfloat16)       # MLA: one RoPE key shared by all heads
     v = torch.randn(T, H, 128).to(torch.bfloat16)
@@ -300,7 +303,7 @@ def test_attn_prefill(lens, masked):
         for m in masks:
             m.fill_diagonal_(True)
     out = prefill_attention(q.to(DEV), k.to(DEV), v.to(DEV), cu, 192 ** -0.5,
-                            [m.to(DEV) for m in masks] if masks else None)
+                            [m.to(DEV) for m in masks] if masks else None, version=version)
     torch.cuda.synchronize()
     for b in range(len(lens)):
         s, t = cu[b], cu[b + 1]
