@@ -514,20 +514,22 @@ __global__ void __launch_bounds__(384, 1) attn_prefill2_kernel(const __grid_cons
       }
       const int k0 = j * BN;
       float mt = -INFINITY;
-      const bool dense_tile = (p.mask == nullptr) && (k0 + BN - 1 <= qt0);
-      if (dense_tile) {
+      uint32_t mw[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
+      if (p.mask && qi < seq_len) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int wi = (k0 >> 5) + c;
+          mw[c] = wi < p.mask_words ? p.mask[size_t(tok) * p.mask_words + wi] : 0u;
+        }
+      }
+      // no per-key work when every row of the warp sees all 128 keys (below the diagonal, mask words all ones:
+      // e.g. DSA rows with fewer candidates than top-k)
+      const bool full_row = (k0 + BN - 1 <= qi) && ((mw[0] & mw[1] & mw[2] & mw[3]) == 0xffffffffu);
+      if (__all_sync(0xffffffffu, full_row)) {
 #pragma unroll
         for (int i = 0; i < 128; ++i) mt = fmaxf(mt, sv[i]);
         mt *= p.scale_log2;
       } else {
-        uint32_t mw[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
-        if (p.mask && qi < seq_len) {
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int wi = (k0 >> 5) + c;
-            mw[c] = wi < p.mask_words ? p.mask[size_t(tok) * p.mask_words + wi] : 0u;
-          }
-        }
 #pragma unroll
         for (int i = 0; i < 128; ++i) {
           const bool allowed = (k0 + i <= qi) && ((mw[i >> 5] >> (i & 31)) & 1u);

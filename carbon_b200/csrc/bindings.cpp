@@ -39,7 +39,8 @@ T* ptr_or_null(const c10::optional<torch::Tensor>& t) {
 int64_t sf_words(int64_t M, int64_t K) { return ((K + 511) / 512) * ((M + 127) / 128) * 128; }
 
 // ---------------------------------------------------------------------------------------------------------------
-void act_quant(torch::Tensor x, torch::Tensor q, torch::Tensor sf, c10::optional<torch::Tensor> src_rows, int64_t M) {
+void act_quant(torch::Tensor x, torch::Tensor q, torch::Tensor sf, c10::optional<torch::Tensor> src_rows, int64_t M,
+               c10::optional<torch::Tensor> n_blocks) {
   CHECK_CUDA(x); CHECK_DT(x, at::kBFloat16); CHECK_DT(q, at::kFloat8_e4m3fn); CHECK_DT(sf, at::kInt);
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1);
   const int K = x.size(1);
@@ -48,7 +49,7 @@ void act_quant(torch::Tensor x, torch::Tensor q, torch::Tensor sf, c10::optional
   if (!src_rows.has_value()) TORCH_CHECK(x.size(0) >= M);
   c10::cuda::CUDAGuard g(x.device());
   CK(cb::act_quant(x.data_ptr(), x.stride(0), q.data_ptr(), K, reinterpret_cast<uint32_t*>(sf.data_ptr()), M, K,
-                   ptr_or_null<const int>(src_rows), cur_stream()));
+                   ptr_or_null<const int>(src_rows), cur_stream(), ptr_or_null<const int>(n_blocks)));
 }
 
 void rms_norm(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> y, c10::optional<torch::Tensor> q,
@@ -84,14 +85,16 @@ void router_topk(torch::Tensor logits, c10::optional<torch::Tensor> bias, int64_
 }
 
 void moe_layout(torch::Tensor ids, int64_t E, torch::Tensor slot_pos, torch::Tensor row_src,
-                torch::Tensor m_block_expert, torch::Tensor num_blocks, c10::optional<torch::Tensor> counts,
-                int64_t align) {
+                torch::Tensor m_block_expert, torch::Tensor num_blocks, torch::Tensor counts, int64_t align,
+                torch::Tensor scratch) {
+  TORCH_CHECK(counts.numel() >= E && scratch.numel() >= 2 * E && scratch.scalar_type() == at::kInt);
   CHECK_CUDA(ids); CHECK_DT(ids, at::kInt); CHECK_CONTIG(ids);
   TORCH_CHECK(row_src.numel() >= m_block_expert.numel() * 128);
   c10::cuda::CUDAGuard g(ids.device());
   CK(cb::moe_layout(ids.data_ptr<int>(), ids.size(0), ids.size(1), E, m_block_expert.numel(),
                     slot_pos.data_ptr<int>(), row_src.data_ptr<int>(), m_block_expert.data_ptr<int>(),
-                    num_blocks.data_ptr<int>(), ptr_or_null<int>(counts), cur_stream(), int(align)));
+                    num_blocks.data_ptr<int>(), counts.data_ptr<int>(), cur_stream(), int(align),
+                    scratch.data_ptr<int>()));
 }
 
 void moe_combine(torch::Tensor Y, torch::Tensor w, torch::Tensor slot_pos, c10::optional<torch::Tensor> add,
@@ -193,11 +196,16 @@ void gemm_fp8(torch::Tensor A, torch::Tensor sfa, torch::Tensor B, torch::Tensor
   }
   if (grouped) TORCH_CHECK(m_block_expert->numel() * 128 <= M, "grouped rows must cover all m blocks");
   c10::cuda::CUDAGuard g(A.device());
+  torch::Tensor work;
+  const bool pair_path = epi != cb::GEMM_OUT_F32 && (pair == 1 || (pair < 0 && !grouped && M >= 512));
+  const int splits = pair_path ? 1 : cb::gemm_fp8_splits(M, N, K, grouped, int(epi), num_sms());
+  if (splits > 1) work = torch::empty({int64_t(splits) * M * N}, A.options().dtype(at::kFloat));
   CK(cb::gemm_fp8(A.data_ptr(), B.data_ptr(), reinterpret_cast<uint32_t*>(sfa.data_ptr()),
                   reinterpret_cast<uint32_t*>(sfb.data_ptr()), M, N, K, Nb, out.data_ptr(), out.stride(0), epi,
                   ptr_or_null<uint32_t>(out_sf), float(swiglu_limit), ptr_or_null<const int>(m_block_expert),
                   ptr_or_null<const int>(num_m_blocks), grouped ? m_block_expert->numel() : 0,
-                  ptr_or_null<int>(status), num_sms(), cur_stream(), int(pair)));
+                  ptr_or_null<int>(status), num_sms(), cur_stream(), int(pair),
+                  splits > 1 ? work.data_ptr<float>() : nullptr));
 }
 
 void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor out, int64_t epi,

@@ -103,6 +103,79 @@ static cudaError_t splitk_reduce(const float* part, int splits, int M, int N, in
   return cudaGetLastError();
 }
 
+// Split-K partial slabs [splits][M][N] (fp32) -> output.  MODE 0: fp32, MODE 1: bf16; 4 columns per thread.
+template <int MODE>
+__global__ void splitk_reduce_out_kernel(const float* __restrict__ part, int splits, int M, int N, void* out,
+                                         int ldo) {
+  const int64_t total4 = int64_t(M) * (N / 4);
+  for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total4; i += int64_t(gridDim.x) * blockDim.x) {
+    const int r = int(i / (N / 4)), c = int(i % (N / 4)) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int sp = 0; sp < splits; ++sp) {
+      const float4 v = *reinterpret_cast<const float4*>(part + (size_t(sp) * M + r) * N + c);
+      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+    }
+    if (MODE == 0) {
+      *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + size_t(r) * ldo + c) = acc;
+    } else {
+      uint2 w = make_uint2(pack_bf16x2(acc.x, acc.y), pack_bf16x2(acc.z, acc.w));
+      *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(out) + size_t(r) * ldo + c) = w;
+    }
+  }
+}
+
+// Split-K partials of an interleaved gate/up GEMM (N = 2I, 128-column chunks gate|up) -> SwiGLU -> fp8 + SF tiles,
+// exactly the SwiGLU epilogue's arithmetic.  One warp per (row, 128 output columns), 4 outputs per lane.
+__global__ void splitk_reduce_swiglu_kernel(const float* __restrict__ part, int splits, int M, int N, float limit,
+                                            uint8_t* __restrict__ out, int ldo, uint32_t* __restrict__ out_sf,
+                                            int sf_row_blocks) {
+  const int I = N / 2, chunks = I / 128;
+  const int wg = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (wg >= M * chunks) return;
+  const int row = wg / chunks, g = wg % chunks;
+  float a[4];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int t = 4 * lane + i;
+    float gv = 0.f, uv = 0.f;
+    for (int sp = 0; sp < splits; ++sp) {
+      const float* pr = part + (size_t(sp) * M + row) * N + 256 * g;
+      gv += pr[t];
+      uv += pr[128 + t];
+    }
+    if (limit > 0.f) { gv = fminf(gv, limit); uv = fminf(fmaxf(uv, -limit), limit); }
+    a[i] = gv / (1.f + __expf(-gv)) * uv;
+    amax = fmaxf(amax, fabsf(a[i]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const uint32_t sb = ue8m0_for_amax(amax);
+  const float inv = ue8m0_inv(sb);
+  *reinterpret_cast<uint32_t*>(out + size_t(row) * ldo + 128 * g + 4 * lane) =
+      pack_fp8x4(a[0] * inv, a[1] * inv, a[2] * inv, a[3] * inv);
+  if (lane == 0) {
+    const int rb = row / 128, r = row % 128;
+    uint8_t* sf = reinterpret_cast<uint8_t*>(out_sf) +
+                  ((size_t(g >> 2) * sf_row_blocks + rb) * 128 + (r % 32) * 4 + (r / 32)) * 4 + (g & 3);
+    *sf = uint8_t(sb);
+  }
+}
+
+// K splits for a dense fp8 GEMM whose output tiles cannot occupy the SMs (decode-sized M): whole 512-wide scale
+// groups per split, enough splits to give every SM a tile.  1 = no split.
+int gemm_fp8_splits(int M, int N, int K, bool grouped, int epi, int num_sms) {
+  if (grouped || M > 256) return 1;
+  const int tiles = ceil_div(M, 128) * ceil_div(N, 128);
+  const int kgroups = ceil_div(K, 512);
+  if (tiles * 2 > num_sms || kgroups < 2) return 1;
+  int sp = ceil_div(num_sms, tiles);
+  sp = sp < kgroups ? sp : kgroups;
+  (void)epi;
+  return sp;
+}
+
 template <int KIND, int EPI, int BN, int ST, int ACC>
 static cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, int max_tiles,
                           int num_sms, cudaStream_t s) {
@@ -123,7 +196,7 @@ static cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const Ge
 cudaError_t gemm_fp8(const void* A, const void* B, const uint32_t* sfa, const uint32_t* sfb, int M, int N, int K,
                      int Nb, void* out, int ldo, int epi, uint32_t* out_sf, float swiglu_limit,
                      const int* m_block_expert, const int* num_m_blocks_dev, int max_m_blocks, int* status,
-                     int num_sms, cudaStream_t s, int pair) {
+                     int num_sms, cudaStream_t s, int pair, float* work) {
   if (M <= 0 || N <= 0) return cudaSuccess;
   if (K % 128 || N % 16) return cudaErrorInvalidValue;
   // pair-tile kernel: dense prefill-sized GEMMs, and grouped GEMMs whose expert segments are 256-row aligned
@@ -149,6 +222,38 @@ cudaError_t gemm_fp8(const void* A, const void* B, const uint32_t* sfa, const ui
     if (epi == GEMM_OUT_SWIGLU_FP8)
       return launch_pair<KIND_MXF8, EPI_SWIGLU_FP8, 2, 6>(ta, tb, tsa, tsb, p, units, num_sms, s);
     return launch_pair<KIND_MXF8, EPI_BF16, 2, 6>(ta, tb, tsa, tsb, p, units, num_sms, s);
+  }
+  const int splits = work ? gemm_fp8_splits(M, N, K, m_block_expert != nullptr, epi, num_sms) : 1;
+  if (splits > 1) {
+    // partial slabs of K ranges (fp32, one 128x128 tile per CTA), then an ordered reduction into the output
+    CUtensorMap ta, tb;
+    if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, K, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, Nb, K, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+      return cudaErrorInvalidValue;
+    GemmParams p{};
+    p.M = M; p.N = N; p.K = K;
+    p.sfa = sfa; p.sfb = sfb;
+    p.sfa_row_blocks = ceil_div(M, 128);
+    p.sfb_row_blocks = ceil_div(Nb, 128);
+    p.out = work; p.ldo = N; p.status = status;
+    p.k_splits = splits;
+    const int tiles = ceil_div(M, 128) * ceil_div(N, 128);
+    cudaError_t e = launch<KIND_MXF8, EPI_F32, 128, 6, 2>(ta, tb, p, tiles * splits, num_sms, s);
+    if (e != cudaSuccess) return e;
+    const int nk_total = ceil_div(K, 128), nk_per = ceil_div(ceil_div(nk_total, splits), 4) * 4;
+    const int used = ceil_div(nk_total, nk_per);
+    if (epi == GEMM_OUT_SWIGLU_FP8) {
+      const int warps = M * (N / 256);
+      splitk_reduce_swiglu_kernel<<<ceil_div(warps, 8), 256, 0, s>>>(work, used, M, N, swiglu_limit,
+                                                                     reinterpret_cast<uint8_t*>(out), ldo, out_sf,
+                                                                     ceil_div(M, 128));
+    } else {
+      const int64_t total4 = int64_t(M) * (N / 4);
+      const int blocks = int(total4 / 256 + 1 < 1024 ? total4 / 256 + 1 : 1024);
+      if (epi == GEMM_OUT_F32) splitk_reduce_out_kernel<0><<<blocks, 256, 0, s>>>(work, used, M, N, out, ldo);
+      else splitk_reduce_out_kernel<1><<<blocks, 256, 0, s>>>(work, used, M, N, out, ldo);
+    }
+    return cudaGetLastError();
   }
   const int BN = (epi == GEMM_OUT_SWIGLU_FP8) ? 256 : 128;
   if (m_block_expert && (N % BN)) return cudaErrorInvalidValue;

@@ -23,11 +23,12 @@ CB_DEVICE size_t sf_byte_offset(int row, int kb, int row_blocks) {
 // ---------------------------------------------------------------------------------------------------------------
 __global__ void act_quant_kernel(const __nv_bfloat16* __restrict__ x, int ldx, uint8_t* __restrict__ q, int ldq,
                                  uint32_t* __restrict__ sf, int M, int K, int row_blocks,
-                                 const int* __restrict__ src_rows, int M_pad) {
+                                 const int* __restrict__ src_rows, int M_pad, const int* __restrict__ n_blocks) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.y * 8 + warp;
   const int kg = blockIdx.x;
   if (row >= M_pad) return;
+  if (n_blocks && row >= n_blocks[0] * 128) return;   // rows past the used 128-row blocks are never read
   int src = row < M ? row : -1;
   if (src >= 0 && src_rows) src = src_rows[row];
   uint32_t word = 0;
@@ -78,11 +79,12 @@ __global__ void act_quant_kernel(const __nv_bfloat16* __restrict__ x, int ldx, u
 }
 
 cudaError_t act_quant(const void* x, int ldx, void* q, int ldq, uint32_t* sf, int M, int K, const int* src_rows,
-                      cudaStream_t s) {
+                      cudaStream_t s, const int* n_blocks) {
   const int row_blocks = ceil_div(M, 128), M_pad = row_blocks * 128;
   dim3 grid(ceil_div(K, 512), ceil_div(M_pad, 8));
   act_quant_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx,
-                                        reinterpret_cast<uint8_t*>(q), ldq, sf, M, K, row_blocks, src_rows, M_pad);
+                                        reinterpret_cast<uint8_t*>(q), ldq, sf, M, K, row_blocks, src_rows, M_pad,
+                                        n_blocks);
   return cudaGetLastError();
 }
 
@@ -296,56 +298,92 @@ cudaError_t router_topk(const float* logits, const float* bias, int T, int E, in
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// MoE layout: expert-sorted rows, every expert segment padded to 128 rows.
-//   ids [T*k] -> counts[E], seg_start[E], m_block_expert[max_blocks], num_blocks[1],
-//   slot_pos [T*k] (row of each (token, slot)), row_src [max_rows] (token of each row, -1 = padding).
-// One CTA of 1024 threads; E <= 1024.
-// ---------------------------------------------------------------------------------------------------------------
-__global__ void moe_layout_kernel(const int* __restrict__ ids, int Tk, int k, int E, int max_blocks,
-                                  int* __restrict__ slot_pos, int* __restrict__ row_src,
-                                  int* __restrict__ m_block_expert, int* __restrict__ num_blocks,
-                                  int* __restrict__ counts_out, int align) {
-  __shared__ int cnt[1024];
-  __shared__ int start[1024];
-  __shared__ int fill[1024];
-  for (int e = threadIdx.x; e < E; e += blockDim.x) { cnt[e] = 0; fill[e] = 0; }
+// MoE layout: expert-sorted rows, every expert segment padded to `align` rows (128, or 256 for CTA-pair GEMM
+// tiles), 128-row blocks tagged with their expert.  Three grid-wide steps: per-expert counts, segment offsets (one
+// CTA scans the padded counts and tags the blocks), scatter of (token, slot) pairs.  Row order inside an expert
+// segment is arbitrary (every row's GEMM result is independent of its position and the combine is per token).
+__global__ void moe_count_local_kernel(const int* __restrict__ ids, int Tk, int E, int* __restrict__ cnt) {
+  extern __shared__ int hcnt[];
+  for (int e = threadIdx.x; e < E; e += blockDim.x) hcnt[e] = 0;
   __syncthreads();
-  for (int i = threadIdx.x; i < Tk; i += blockDim.x) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < Tk; i += gridDim.x * blockDim.x) {
     const int e = ids[i];
-    if (e >= 0 && e < E) atomicAdd(&cnt[e], 1);
+    if (e >= 0 && e < E) atomicAdd(&hcnt[e], 1);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int acc = 0;
-    for (int e = 0; e < E; ++e) { start[e] = acc; acc += (cnt[e] + align - 1) / align * align; }
-    const int nb = acc >> 7;
-    num_blocks[0] = nb;
-    for (int e = 0, b = 0; e < E; ++e) {
-      const int nbe = (cnt[e] + align - 1) / align * (align >> 7);
-      for (int j = 0; j < nbe && b < max_blocks; ++j) m_block_expert[b++] = e;
+  for (int e = threadIdx.x; e < E; e += blockDim.x)
+    if (hcnt[e]) atomicAdd(&cnt[e], hcnt[e]);
+}
+
+__global__ void moe_offsets_kernel(const int* __restrict__ cnt, int E, int align, int max_blocks,
+                                   int* __restrict__ start, int* __restrict__ fill, int* __restrict__ m_block_expert,
+                                   int* __restrict__ num_blocks, int* __restrict__ row_src) {
+  __shared__ int wsum[32];
+  __shared__ int s_total;
+  const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
+  const int c = t < E ? cnt[t] : 0;
+  const int padded = (c + align - 1) / align * align;
+  int v = padded;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += n;
+  }
+  if (lane == 31) wsum[wid] = v;
+  __syncthreads();
+  if (wid == 0) {
+    int w = lane < int(blockDim.x >> 5) ? wsum[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += n;
     }
-    for (int b = nb; b < max_blocks; ++b) m_block_expert[b] = -1;
+    wsum[lane] = w;
+    if (lane == 31) s_total = w;
   }
   __syncthreads();
-  for (int e = threadIdx.x; e < E; e += blockDim.x) if (counts_out) counts_out[e] = cnt[e];
+  const int incl = v + (wid > 0 ? wsum[wid - 1] : 0);
+  const int st = incl - padded;
   const int max_rows = max_blocks * 128;
-  for (int r = threadIdx.x; r < max_rows; r += blockDim.x) row_src[r] = -1;
-  __syncthreads();
-  for (int i = threadIdx.x; i < Tk; i += blockDim.x) {
+  if (t < E) {
+    start[t] = st;
+    fill[t] = 0;
+    for (int b = st >> 7; b < (st + padded) >> 7 && b < max_blocks; ++b) m_block_expert[b] = t;
+    for (int r = st + c; r < st + padded && r < max_rows; ++r) row_src[r] = -1;   // padding rows
+  }
+  const int total_blocks = s_total >> 7;
+  if (t == 0) num_blocks[0] = total_blocks;
+  for (int b = total_blocks + t; b < max_blocks; b += blockDim.x) m_block_expert[b] = -1;
+}
+
+__global__ void moe_scatter_kernel(const int* __restrict__ ids, int Tk, int k, int E, const int* __restrict__ start,
+                                   int* __restrict__ fill, int max_rows, int* __restrict__ slot_pos,
+                                   int* __restrict__ row_src) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < Tk; i += gridDim.x * blockDim.x) {
     const int e = ids[i];
     int pos = -1;
     if (e >= 0 && e < E) {
       pos = start[e] + atomicAdd(&fill[e], 1);
       if (pos < max_rows) row_src[pos] = i / k;
+      else pos = -1;
     }
     slot_pos[i] = pos;
   }
 }
+
+// counts [E] (output), scratch [2E] (segment starts, fill counters)
 cudaError_t moe_layout(const int* ids, int T, int k, int E, int max_blocks, int* slot_pos, int* row_src,
-                       int* m_block_expert, int* num_blocks, int* counts, cudaStream_t s, int align) {
-  if (E > 1024 || (align != 128 && align != 256)) return cudaErrorInvalidValue;
-  moe_layout_kernel<<<1, 1024, 0, s>>>(ids, T * k, k, E, max_blocks, slot_pos, row_src, m_block_expert, num_blocks,
-                                       counts, align);
+                       int* m_block_expert, int* num_blocks, int* counts, cudaStream_t s, int align, int* scratch) {
+  if (E > 1024 || (align != 128 && align != 256) || !counts || !scratch) return cudaErrorInvalidValue;
+  const int Tk = T * k;
+  cudaError_t e = cudaMemsetAsync(counts, 0, sizeof(int) * E, s);
+  if (e != cudaSuccess) return e;
+  const int blocks = Tk / 1024 + 1 < 148 ? Tk / 1024 + 1 : 148;
+  moe_count_local_kernel<<<blocks, 256, E * sizeof(int), s>>>(ids, Tk, E, counts);
+  moe_offsets_kernel<<<1, 1024, 0, s>>>(counts, E, align, max_blocks, scratch, scratch + E, m_block_expert,
+                                        num_blocks, row_src);
+  moe_scatter_kernel<<<blocks, 256, 0, s>>>(ids, Tk, k, E, scratch, scratch + E, max_blocks * 128, slot_pos,
+                                            row_src);
   return cudaGetLastError();
 }
 

@@ -7,7 +7,7 @@
 namespace cb {
 
 cudaError_t act_quant(const void* x, int ldx, void* q, int ldq, uint32_t* sf, int M, int K, const int* src_rows,
-                      cudaStream_t s);
+                      cudaStream_t s, const int* n_blocks = nullptr);
 cudaError_t rms_norm(const void* x, int ldx, const float* w, void* y, int ldy, void* q, uint32_t* sf, int M, int D,
                      float eps, cudaStream_t s);
 cudaError_t sf_pad(uint32_t* sf, int M, int K, cudaStream_t s);
@@ -16,7 +16,7 @@ cudaError_t rope_inplace(void* x, int T, int64_t stride_t, int64_t stride_h, int
 cudaError_t router_topk(const float* logits, const float* bias, int T, int E, int k, int score, bool norm,
                         float route_scale, float* w, int* ids, cudaStream_t s);
 cudaError_t moe_layout(const int* ids, int T, int k, int E, int max_blocks, int* slot_pos, int* row_src,
-                       int* m_block_expert, int* num_blocks, int* counts, cudaStream_t s, int align = 128);
+                       int* m_block_expert, int* num_blocks, int* counts, cudaStream_t s, int align, int* scratch);
 cudaError_t moe_combine(const void* Y, int ldy, const float* w, const int* slot_pos, int T, int k, const void* add,
                         void* out, int D, cudaStream_t s);
 cudaError_t mhc_coeffs(const float* mix, int ld_mix, const float* sumsq, const float* base, const float* scale, int T,
@@ -39,7 +39,9 @@ enum GemmEpiHost { GEMM_OUT_BF16 = 0, GEMM_OUT_SWIGLU_FP8 = 1, GEMM_OUT_F32 = 2 
 cudaError_t gemm_fp8(const void* A, const void* B, const uint32_t* sfa, const uint32_t* sfb, int M, int N, int K,
                      int Nb, void* out, int ldo, int epi, uint32_t* out_sf, float swiglu_limit,
                      const int* m_block_expert, const int* num_m_blocks_dev, int max_m_blocks, int* status,
-                     int num_sms, cudaStream_t s, int pair = -1);
+                     int num_sms, cudaStream_t s, int pair = -1, float* work = nullptr);
+// K splits gemm_fp8 uses for a dense small-M GEMM (work must then hold splits * M * N floats).
+int gemm_fp8_splits(int M, int N, int K, bool grouped, int epi, int num_sms);
 cudaError_t gemm_bf16(const void* A, int lda, const void* B, int ldb, int M, int N, int K, int Nb, void* out, int ldo,
                       int epi, const int* m_block_expert, const int* num_m_blocks_dev, int max_m_blocks, int* status,
                       int num_sms, cudaStream_t s, int k_splits = 1, float* work = nullptr);

@@ -437,7 +437,7 @@ class DeepseekModel:
             return out + shared if shared is not None else out
         with region("moe.dispatch"):
             lay = C.MoeLayout(ids, self.E_local)
-            a_q, a_sf = quant_act(h, src_rows=lay.row_src)
+            a_q, a_sf = quant_act(h, src_rows=lay.row_src, n_blocks=lay.num_blocks)
         I2 = 2 * cfg.moe_intermediate
         with region("moe.gemm_up"):
             act, act_sf = fp8_gemm_swiglu(a_q, a_sf, L.e_w13, cfg.swiglu_limit, lay.m_block_expert, lay.num_blocks,

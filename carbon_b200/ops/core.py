@@ -104,8 +104,9 @@ class MoeLayout:
         self.num_blocks = torch.empty(1, dtype=torch.int32, device=dev)
         self.counts = torch.empty(n_experts, dtype=torch.int32, device=dev)
         if ids.is_cuda:
+            scratch = torch.empty(2 * n_experts, dtype=torch.int32, device=dev)
             ext().moe_layout(ids.contiguous(), n_experts, self.slot_pos, self.row_src, self.m_block_expert,
-                             self.num_blocks, self.counts, align)
+                             self.num_blocks, self.counts, align, scratch)
         else:
             self._cpu(ids)
 

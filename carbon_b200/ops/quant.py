@@ -89,8 +89,10 @@ class Fp8Weight:
         return Fp8Weight(q.contiguous(), pack_sf(rows), scale)
 
 
-def quant_act(x: torch.Tensor, src_rows: Optional[torch.Tensor] = None, M: Optional[int] = None):
-    """bf16 [T, K] -> (fp8 [M, K], SF tiles). With ``src_rows`` ([M] int32, -1 = zero row) rows are gathered."""
+def quant_act(x: torch.Tensor, src_rows: Optional[torch.Tensor] = None, M: Optional[int] = None,
+              n_blocks: Optional[torch.Tensor] = None):
+    """bf16 [T, K] -> (fp8 [M, K], SF tiles). With ``src_rows`` ([M] int32, -1 = zero row) rows are gathered;
+    ``n_blocks`` (device int32) limits the work to the first n_blocks * 128 rows (the rest is left unwritten)."""
     if not x.is_cuda:
         xs = x.float() if src_rows is None else torch.where(
             (src_rows >= 0)[:, None], x.float()[src_rows.clamp(min=0).long()], torch.zeros(()))
@@ -102,7 +104,7 @@ def quant_act(x: torch.Tensor, src_rows: Optional[torch.Tensor] = None, M: Optio
     K = x.shape[1]
     q = torch.empty(M, K, dtype=torch.float8_e4m3fn, device=x.device)
     sf = empty_sf(M, K, x.device)
-    ext().act_quant(x, q, sf, src_rows, M)
+    ext().act_quant(x, q, sf, src_rows, M, n_blocks)
     return q, sf
 
 
