@@ -49,7 +49,19 @@ void act_quant(torch::Tensor x, torch::Tensor q, torch::Tensor sf, c10::optional
   if (!src_rows.has_value()) TORCH_CHECK(x.size(0) >= M);
   c10::cuda::CUDAGuard g(x.device());
   CK(cb::act_quant(x.data_ptr(), x.stride(0), q.data_ptr(), K, reinterpret_cast<uint32_t*>(sf.data_ptr()), M, K,
-                   ptr_or_null<const int>(src_rows), cur_stream(), ptr_or_null<const int>(n_blocks)));
+                   ptr_or_null<const int>(src_rows), cur_stream(), ptr_or_null<const int>(n_blocks), int(x.size(0))));
+}
+
+void gather_fp8_rows(torch::Tensor src, torch::Tensor src_sf, torch::Tensor src_rows, torch::Tensor dst,
+                     torch::Tensor dst_sf, c10::optional<torch::Tensor> n_blocks) {
+  CHECK_CUDA(src); CHECK_DT(src, at::kFloat8_e4m3fn); CHECK_DT(dst, at::kFloat8_e4m3fn); CHECK_CONTIG(src);
+  CHECK_CONTIG(dst); CHECK_DT(src_rows, at::kInt);
+  const int K = src.size(1), M = dst.size(0);
+  TORCH_CHECK(dst.size(1) == K && src_rows.numel() >= M && dst_sf.numel() >= sf_words(M, K));
+  c10::cuda::CUDAGuard g(src.device());
+  CK(cb::gather_fp8_rows(src.data_ptr(), reinterpret_cast<const uint32_t*>(src_sf.data_ptr()), src.size(0), K,
+                         src_rows.data_ptr<int>(), M, ptr_or_null<const int>(n_blocks), dst.data_ptr(),
+                         reinterpret_cast<uint32_t*>(dst_sf.data_ptr()), cur_stream()));
 }
 
 void rms_norm(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> y, c10::optional<torch::Tensor> q,
@@ -316,6 +328,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope", &rope);
   m.def("router_topk", &router_topk);
   m.def("moe_layout", &moe_layout);
+  m.def("gather_fp8_rows", &gather_fp8_rows);
   m.def("moe_combine", &moe_combine);
   m.def("mhc_coeffs", &mhc_coeffs);
   m.def("mhc_head_coeffs", &mhc_head_coeffs);

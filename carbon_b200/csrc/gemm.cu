@@ -170,10 +170,18 @@ int gemm_fp8_splits(int M, int N, int K, bool grouped, int epi, int num_sms) {
   const int tiles = ceil_div(M, 128) * ceil_div(N, 128);
   const int kgroups = ceil_div(K, 512);
   if (tiles * 2 > num_sms || kgroups < 2) return 1;
-  int sp = ceil_div(num_sms, tiles);
-  sp = sp < kgroups ? sp : kgroups;
+  // the persistent grid runs tiles*splits work items on num_sms CTAs: pick the split count whose last wave is
+  // fullest (ties -> fewer splits, less partial traffic)
+  int best = 1;
+  float best_eff = 0.f;
+  for (int sp = 2; sp <= kgroups && sp <= 32; ++sp) {
+    const int items = tiles * sp;
+    const int waves = ceil_div(items, num_sms);
+    const float eff = float(items) / float(waves * num_sms);
+    if (eff > best_eff + 0.02f) { best = sp; best_eff = eff; }
+  }
   (void)epi;
-  return sp;
+  return best;
 }
 
 template <int KIND, int EPI, int BN, int ST, int ACC>

@@ -23,7 +23,8 @@ CB_DEVICE size_t sf_byte_offset(int row, int kb, int row_blocks) {
 // ---------------------------------------------------------------------------------------------------------------
 __global__ void act_quant_kernel(const __nv_bfloat16* __restrict__ x, int ldx, uint8_t* __restrict__ q, int ldq,
                                  uint32_t* __restrict__ sf, int M, int K, int row_blocks,
-                                 const int* __restrict__ src_rows, int M_pad, const int* __restrict__ n_blocks) {
+                                 const int* __restrict__ src_rows, int M_pad, const int* __restrict__ n_blocks,
+                                 int x_rows) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.y * 8 + warp;
   const int kg = blockIdx.x;
@@ -31,6 +32,7 @@ __global__ void act_quant_kernel(const __nv_bfloat16* __restrict__ x, int ldx, u
   if (n_blocks && row >= n_blocks[0] * 128) return;   // rows past the used 128-row blocks are never read
   int src = row < M ? row : -1;
   if (src >= 0 && src_rows) src = src_rows[row];
+  if (src >= x_rows) src = -1;                   // anything but a valid source row quantises as a zero row
   uint32_t word = 0;
 #pragma unroll
   for (int h = 0; h < 2; ++h) {                  // two halves of 256 columns = two k-blocks each
@@ -79,12 +81,47 @@ __global__ void act_quant_kernel(const __nv_bfloat16* __restrict__ x, int ldx, u
 }
 
 cudaError_t act_quant(const void* x, int ldx, void* q, int ldq, uint32_t* sf, int M, int K, const int* src_rows,
-                      cudaStream_t s, const int* n_blocks) {
+                      cudaStream_t s, const int* n_blocks, int x_rows) {
+  if (x_rows < 0) x_rows = 0x7fffffff;
   const int row_blocks = ceil_div(M, 128), M_pad = row_blocks * 128;
   dim3 grid(ceil_div(K, 512), ceil_div(M_pad, 8));
   act_quant_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx,
                                         reinterpret_cast<uint8_t*>(q), ldq, sf, M, K, row_blocks, src_rows, M_pad,
-                                        n_blocks);
+                                        n_blocks, x_rows);
+  return cudaGetLastError();
+}
+
+// Gather of already-quantised rows: dst row r = src row src_rows[r] (fp8 bytes and its SF words; -1 = zero row with
+// unit scales).  One warp per destination row; rows past n_blocks*128 are left alone.  Used by the MoE dispatch so
+// that every token is quantised once instead of once per selected expert.
+__global__ void gather_fp8_rows_kernel(const uint8_t* __restrict__ src, const uint32_t* __restrict__ src_sf,
+                                       int src_rows_n, int K, const int* __restrict__ src_rows, int M,
+                                       const int* __restrict__ n_blocks, uint8_t* __restrict__ dst,
+                                       uint32_t* __restrict__ dst_sf) {
+  const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  if (n_blocks && row >= n_blocks[0] * 128) return;
+  int sr = src_rows[row];
+  if (sr >= src_rows_n) sr = -1;
+  const uint4* s4 = reinterpret_cast<const uint4*>(src + size_t(sr < 0 ? 0 : sr) * K);
+  uint4* d4 = reinterpret_cast<uint4*>(dst + size_t(row) * K);
+  for (int c = lane; c < K / 16; c += 32) d4[c] = sr < 0 ? make_uint4(0, 0, 0, 0) : s4[c];
+  const int kgroups = (K + 511) / 512;
+  const int src_rb = (src_rows_n + 127) / 128, dst_rb = (M + 127) / 128;
+  for (int kg = lane; kg < kgroups; kg += 32) {
+    uint32_t w = 0x7f7f7f7fu;                       // unit scales for a zero row
+    if (sr >= 0) w = src_sf[(size_t(kg) * src_rb + (sr >> 7)) * 128 + (sr & 31) * 4 + ((sr & 127) >> 5)];
+    dst_sf[(size_t(kg) * dst_rb + (row >> 7)) * 128 + (row & 31) * 4 + ((row & 127) >> 5)] = w;
+  }
+}
+
+cudaError_t gather_fp8_rows(const void* src, const uint32_t* src_sf, int src_rows_n, int K, const int* src_rows,
+                            int M, const int* n_blocks, void* dst, uint32_t* dst_sf, cudaStream_t s) {
+  if (K % 16) return cudaErrorInvalidValue;
+  gather_fp8_rows_kernel<<<ceil_div(M, 8), 256, 0, s>>>(reinterpret_cast<const uint8_t*>(src), src_sf, src_rows_n,
+                                                        K, src_rows, M, n_blocks, reinterpret_cast<uint8_t*>(dst),
+                                                        dst_sf);
   return cudaGetLastError();
 }
 
@@ -354,6 +391,7 @@ __global__ void moe_offsets_kernel(const int* __restrict__ cnt, int E, int align
   const int total_blocks = s_total >> 7;
   if (t == 0) num_blocks[0] = total_blocks;
   for (int b = total_blocks + t; b < max_blocks; b += blockDim.x) m_block_expert[b] = -1;
+  for (int r = s_total + t; r < max_rows; r += blockDim.x) row_src[r] = -1;   // rows past the used blocks
 }
 
 __global__ void moe_scatter_kernel(const int* __restrict__ ids, int Tk, int k, int E, const int* __restrict__ start,

@@ -6,8 +6,11 @@
 
 namespace cb {
 
+// x_rows: rows of x; gather sources outside [0, x_rows) give zero rows (-1: not checked).
 cudaError_t act_quant(const void* x, int ldx, void* q, int ldq, uint32_t* sf, int M, int K, const int* src_rows,
-                      cudaStream_t s, const int* n_blocks = nullptr);
+                      cudaStream_t s, const int* n_blocks = nullptr, int x_rows = -1);
+cudaError_t gather_fp8_rows(const void* src, const uint32_t* src_sf, int src_rows_n, int K, const int* src_rows,
+                            int M, const int* n_blocks, void* dst, uint32_t* dst_sf, cudaStream_t s);
 cudaError_t rms_norm(const void* x, int ldx, const float* w, void* y, int ldy, void* q, uint32_t* sf, int M, int D,
                      float eps, cudaStream_t s);
 cudaError_t sf_pad(uint32_t* sf, int M, int K, cudaStream_t s);

@@ -27,7 +27,7 @@ from ..config import ModelConfig
 from ..ops import attention as A
 from ..ops import core as C
 from ..ops.gemm import bf16_gemm, fp8_gemm, fp8_gemm_swiglu, interleave_gate_up
-from ..ops.quant import Fp8Weight, quant_act, quantize_weight, stack_weights
+from ..ops.quant import Fp8Weight, gather_rows_fp8, quant_act, quantize_weight, stack_weights
 from ..ref import ops as R
 from ..utils.trace import region
 from .weights import WeightSource
@@ -419,9 +419,9 @@ class DeepseekModel:
                     shared = Pending(L.shared(h, xq=hq), self._side)
             else:
                 shared = L.shared(h, xq=hq)
-        return self.pctx.moe(self, L, h, w, ids, shared)
+        return self.pctx.moe(self, L, h, w, ids, shared, hq=hq)
 
-    def moe_local(self, L, h, w, ids, shared):
+    def moe_local(self, L, h, w, ids, shared, hq=None):
         """All experts local (EP = 1): sort rows by expert, grouped GEMMs, weighted combine."""
         cfg = self.cfg
         T, k = ids.shape
@@ -437,7 +437,9 @@ class DeepseekModel:
             return out + shared if shared is not None else out
         with region("moe.dispatch"):
             lay = C.MoeLayout(ids, self.E_local)
-            a_q, a_sf = quant_act(h, src_rows=lay.row_src, n_blocks=lay.num_blocks)
+            # quantise every token once (the shared expert already did when hq is given), then gather rows
+            tq, tsf = hq if hq is not None else quant_act(h)
+            a_q, a_sf = gather_rows_fp8(tq, tsf, lay.row_src, n_blocks=lay.num_blocks)
         I2 = 2 * cfg.moe_intermediate
         with region("moe.gemm_up"):
             act, act_sf = fp8_gemm_swiglu(a_q, a_sf, L.e_w13, cfg.swiglu_limit, lay.m_block_expert, lay.num_blocks,

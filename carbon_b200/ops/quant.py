@@ -108,6 +108,23 @@ def quant_act(x: torch.Tensor, src_rows: Optional[torch.Tensor] = None, M: Optio
     return q, sf
 
 
+def gather_rows_fp8(q: torch.Tensor, sf: torch.Tensor, src_rows: torch.Tensor,
+                    n_blocks: Optional[torch.Tensor] = None):
+    """Rows of an already-quantised matrix (fp8 + SF tiles) gathered by ``src_rows`` (-1 = zero row)."""
+    M, K = src_rows.numel(), q.shape[1]
+    if not q.is_cuda:
+        s = unpack_sf(sf, q.shape[0], K)
+        ok = src_rows >= 0
+        idx = src_rows.clamp(min=0).long()
+        qd = torch.where(ok[:, None], q.view(torch.uint8)[idx], torch.zeros((), dtype=torch.uint8)).view(q.dtype)
+        sd = torch.where(ok[:, None], s[idx], torch.ones(()))
+        return qd, pack_sf(sd)
+    out = torch.empty(M, K, dtype=q.dtype, device=q.device)
+    out_sf = empty_sf(M, K, q.device)
+    ext().gather_fp8_rows(q, sf, src_rows, out, out_sf, n_blocks)
+    return out, out_sf
+
+
 def dequant_act(q: torch.Tensor, sf: torch.Tensor) -> torch.Tensor:
     M, K = q.shape
     s = unpack_sf(sf.cpu(), M, K)

@@ -71,8 +71,8 @@ class ParallelCtx:
     def attn_out(self, x: torch.Tensor) -> torch.Tensor:
         return x
 
-    def moe(self, model, L, h, w, ids, shared):
-        return model.moe_local(L, h, w, ids, shared)
+    def moe(self, model, L, h, w, ids, shared, hq=None):
+        return model.moe_local(L, h, w, ids, shared, hq=hq)
 
     def lm_head(self, model, y: torch.Tensor) -> torch.Tensor:
         return model.head_w(y, out_dtype=torch.float32)

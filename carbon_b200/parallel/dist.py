@@ -142,7 +142,7 @@ class DistCtx(ParallelCtx):
         sumsq = X.float().pow(2).sum((1, 2)) if model.on_gpu else None
         return X, sumsq
 
-    def moe(self, model, L, h, w, ids, shared):
+    def moe(self, model, L, h, w, ids, shared, hq=None):
         """Expert parallel: route rows to their experts' owners (all-to-all), grouped GEMMs there, rows back."""
         El = model.E_local
         T, k = ids.shape

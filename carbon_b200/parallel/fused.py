@@ -182,7 +182,7 @@ class FusedCtx(DistCtx):
             }
         return self._moe
 
-    def moe(self, model, L, h, w, ids, shared):
+    def moe(self, model, L, h, w, ids, shared, hq=None):
         cfg = model.cfg
         e = ext()
         T, k = ids.shape

@@ -1,6 +1,6 @@
 """Small, self-contained kernel cases for profiler captures (one launch of one kernel each, a few GB at most).
 
-    python -m carbon_b200.profile_cases gemm|grouped|attn|decode|indexer
+    python -m carbon_b200.profile_cases gemm|grouped|moe_decode|attn|decode|indexer
 
 Each case sets up inputs larger than L2 where it can, runs its kernel twice (warm-up + the launch to capture) and
 exits 0, so that ``ncu -k regex:<kernel> -s 1 -c 1`` captures exactly one warm launch.
@@ -39,6 +39,22 @@ def grouped():
         m.moe_local(m.layers[0], h, w, ids, None)
 
 
+def moe_decode():
+    """Decode-sized MoE (32 tokens x top-8 over 64 experts): the grouped GEMMs stream expert weights."""
+    from .config import ModelConfig
+    from .models.deepseek import DeepseekModel
+    from .models.weights import WeightSource
+    from .ops import core as C
+
+    cfg = ModelConfig(n_layers=1, n_dense_layers=0, vocab_size=1024, n_routed_experts=64, index_n_heads=0)
+    m = DeepseekModel(cfg, WeightSource(cfg, seed=0), "cuda")
+    h = torch.randn(32, cfg.hidden_size, device="cuda").to(torch.bfloat16)
+    w, ids = C.router_topk(torch.randn(32, 64, device="cuda"), None, 8, "sigmoid", 2.5, True)
+    m.pctx.set_bounds([0, 32])
+    for _ in range(2):
+        m.moe_local(m.layers[0], h, w, ids, None)
+
+
 def attn():
     from .ops.attention import mla_prefill
 
@@ -73,6 +89,7 @@ def indexer():
 
 
 if __name__ == "__main__":
-    {"gemm": gemm, "grouped": grouped, "attn": attn, "decode": decode, "indexer": indexer}[sys.argv[1]]()
+    {"gemm": gemm, "grouped": grouped, "moe_decode": moe_decode, "attn": attn, "decode": decode,
+     "indexer": indexer}[sys.argv[1]]()
     torch.cuda.synchronize()
     print("ok", sys.argv[1])

@@ -213,3 +213,17 @@ def test_small_m_split_k_swiglu(M):
     gu = (R.dequant_fp8_rows(q_ref, s_ref) @ W.dequant().t()).view(M, -1, 2, 128)
     ref = R.swiglu(gu[:, :, 0].reshape(M, -1), gu[:, :, 1].reshape(M, -1))
     assert rel_err(act_d, ref) < 0.04, rel_err(act_d, ref)
+
+
+def test_gather_fp8_rows_matches_gather_quantise():
+    """Quantise-once + row gather (MoE dispatch) == gather + quantise, bitwise, including -1 rows."""
+    from carbon_b200.ops.quant import gather_rows_fp8, quant_act
+
+    x = torch.randn(300, 7168, device=DEV).to(torch.bfloat16)
+    src = torch.randint(-1, 300, (1024,), dtype=torch.int32, device=DEV)
+    q1, sf1 = quant_act(x, src_rows=src)
+    tq, tsf = quant_act(x)
+    q2, sf2 = gather_rows_fp8(tq, tsf, src)
+    torch.cuda.synchronize()
+    assert torch.equal(q1.view(torch.uint8), q2.view(torch.uint8))
+    assert torch.equal(sf1, sf2)
