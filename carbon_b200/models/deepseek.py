@@ -415,6 +415,11 @@ class DeepseekModel:
                 if self._side is None:
                     self._side = torch.cuda.Stream()
                 self._side.wait_stream(torch.cuda.current_stream())
+                # h / hq belong to the main stream's allocator pool: keep them alive until the side stream is done
+                h.record_stream(self._side)
+                if hq is not None:
+                    hq[0].record_stream(self._side)
+                    hq[1].record_stream(self._side)
                 with torch.cuda.stream(self._side), region("moe.shared"):
                     shared = Pending(L.shared(h, xq=hq), self._side)
             else:
