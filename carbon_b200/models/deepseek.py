@@ -442,8 +442,9 @@ class DeepseekModel:
             return out + shared if shared is not None else out
         with region("moe.dispatch"):
             lay = C.MoeLayout(ids, self.E_local)
-            # quantise every token once (the shared expert already did when hq is given), then gather rows
-            tq, tsf = hq if hq is not None else quant_act(h)
+            # quantise every token once, then gather rows; quantised from the bf16 rows like the multi-GPU dispatch
+            # kernels do, so that every parallel layout feeds the experts identical bytes
+            tq, tsf = quant_act(h)
             a_q, a_sf = gather_rows_fp8(tq, tsf, lay.row_src, n_blocks=lay.num_blocks)
         I2 = 2 * cfg.moe_intermediate
         with region("moe.gemm_up"):
