@@ -24,9 +24,14 @@ def _port():
 
 
 def _cfg():
+    """Every token selects all 8 experts and DSA stays dense: the collectives' different rounding (bf16 partial
+    sums on the wire) cannot flip a discrete router or top-k choice, so logits can be compared with a tolerance.
+    The dispatch/combine still moves every row to both ranks' experts; the DSA multi-rank path is checked exactly
+    by the gloo test."""
     from carbon_b200.config import small_gpu_config
 
-    return small_gpu_config().replace(n_layers=2, n_routed_experts=8, n_activated_experts=2, vocab_size=2048)
+    return small_gpu_config().replace(n_layers=2, n_routed_experts=8, n_activated_experts=8, vocab_size=2048,
+                                      index_topk=4096)
 
 
 def _prompts(cfg):
@@ -114,4 +119,5 @@ def test_two_gpu_engine_matches_single_gpu(comm):
         for step, (a, b) in enumerate(zip(hist, hist_ref)):
             a = torch.from_numpy(a)
             rel = ((a - b).norm() / b.norm()).item()
-            assert rel < 0.05, (comm, rank, step, rel)
+            per_row = ((a - b).norm(dim=-1) / b.norm(dim=-1)).tolist()     # one row per request
+            assert rel < 0.05, (comm, rank, step, rel, per_row)
