@@ -43,7 +43,22 @@ struct Params {
   float scale_log2;       // softmax scale * log2(e)
   __nv_bfloat16* out;     // [T, H, DV]
   int* status;
+  // optional event trace of CTA (0,0) (two-tile kernel): [0] = event count, then (clock64, kind<<32 | t<<16 | j)
+  unsigned long long* trace;
+  int trace_cap;
 };
+
+// Records one event of the traced CTA (kinds: 1 MMA saw P ready, 2 MMA issued PV+QK, 3 softmax waits for S,
+// 4 S arrived, 5 P written).
+CB_DEVICE void trace_event(const Params& p, int kind, int t, int j) {
+  if (p.trace == nullptr || blockIdx.x != 0 || blockIdx.y != 0) return;
+  const unsigned long long i = atomicAdd(p.trace, 1ull);
+  if (int(i) < p.trace_cap) {
+    p.trace[1 + 2 * i] = clock64();
+    p.trace[2 + 2 * i] = (static_cast<unsigned long long>(kind) << 32) | (static_cast<unsigned long long>(t) << 16) |
+                         static_cast<unsigned long long>(j);
+  }
+}
 
 // MN-major (V as the B operand, N = dv contiguous) 128B-swizzled descriptor: LBO = bytes between 64-wide dv
 // atoms, SBO = bytes between 8-row key groups.
@@ -472,6 +487,7 @@ __global__ void __launch_bounds__(384, 1) attn_prefill2_kernel(const __grid_cons
         for (int t = 0; t < 2 && ok; ++t) {
           if (j >= n_kt_t[t]) continue;
           if (!mbar_wait(&p_full[t], j & 1)) { fail(kErrTimeoutTmem); ok = false; break; }
+          fa::trace_event(p, 1, t, j);
           tc_fence_after();
           if (!v_ready) { ok = wait_chunks(j * CH_PER_KV + 3, 2); v_ready = true; if (!ok) break; }
           pv(t, j);
@@ -479,6 +495,7 @@ __global__ void __launch_bounds__(384, 1) attn_prefill2_kernel(const __grid_cons
             if (!k_ready) { ok = wait_chunks((j + 1) * CH_PER_KV, 3); k_ready = true; if (!ok) break; }
             qk(t, j + 1);
           }
+          fa::trace_event(p, 2, t, j);
         }
         if (!ok) break;
         release_chunks(j * CH_PER_KV + 3, 2);
@@ -497,8 +514,11 @@ __global__ void __launch_bounds__(384, 1) attn_prefill2_kernel(const __grid_cons
     const int nkt = n_kt_t[t];
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
+    const bool tracer = (q == 0 && lane == 0);
     for (int j = 0; j < nkt; ++j) {
+      if (tracer) fa::trace_event(p, 3, t, j);
       if (!mbar_wait(&s_full[t], j & 1)) { fail(kErrTimeoutTmem); ok = false; break; }
+      if (tracer) fa::trace_event(p, 4, t, j);
       tc_fence_after();
       float sv[128];
       {
@@ -574,6 +594,7 @@ __global__ void __launch_bounds__(384, 1) attn_prefill2_kernel(const __grid_cons
       m_used = m_new;
       tmem_st_wait();
       tc_fence_before();
+      if (tracer) fa::trace_event(p, 5, t, j);
       mbar_arrive(&p_full[t]);
     }
     if (ok && nkt > 0) {
@@ -670,6 +691,8 @@ cudaError_t attn_prefill(const void* q, const void* kvb, const void* kpe, int T,
   p.scale_log2 = scale * 1.4426950408889634f;
   p.out = reinterpret_cast<__nv_bfloat16*>(out);
   p.status = status;
+  p.trace = nullptr;
+  p.trace_cap = 0;
   dim3 grid(n_tiles, H);
   attn_prefill_kernel<<<grid, 384, SMEM, s>>>(tq, tkv, tkpe, p);
   return cudaGetLastError();
@@ -678,7 +701,7 @@ cudaError_t attn_prefill(const void* q, const void* kvb, const void* kpe, int T,
 // Two-tile kernel: tiles are (seq_start, seq_len, q0, 0) with q0 a multiple of 256.
 cudaError_t attn_prefill2(const void* q, const void* kvb, const void* kpe, int T, int H, const int* tiles,
                           int n_tiles, const uint32_t* mask, int mask_words, float scale, void* out, int* status,
-                          cudaStream_t s) {
+                          cudaStream_t s, int64_t* trace, int trace_cap) {
   using namespace fa;
   if (n_tiles == 0) return cudaSuccess;
   CUtensorMap tq, tkv, tkpe;
@@ -702,6 +725,8 @@ cudaError_t attn_prefill2(const void* q, const void* kvb, const void* kpe, int T
   p.scale_log2 = scale * 1.4426950408889634f;
   p.out = reinterpret_cast<__nv_bfloat16*>(out);
   p.status = status;
+  p.trace = reinterpret_cast<unsigned long long*>(trace);
+  p.trace_cap = trace_cap;
   dim3 grid(n_tiles, H);
   fa2::attn_prefill2_kernel<<<grid, 384, fa2::SMEM, s>>>(tq, tkv, tkpe, p);
   return cudaGetLastError();

@@ -187,7 +187,7 @@ void silu_mul(torch::Tensor gu, double limit, torch::Tensor out) {
 void gemm_fp8(torch::Tensor A, torch::Tensor sfa, torch::Tensor B, torch::Tensor sfb, torch::Tensor out, int64_t epi,
               c10::optional<torch::Tensor> out_sf, double swiglu_limit, c10::optional<torch::Tensor> m_block_expert,
               c10::optional<torch::Tensor> num_m_blocks, int64_t N_per_group, c10::optional<torch::Tensor> status,
-              int64_t pair) {
+              int64_t pair, c10::optional<torch::Tensor> row_valid) {
   CHECK_CUDA(A); CHECK_DT(A, at::kFloat8_e4m3fn); CHECK_DT(B, at::kFloat8_e4m3fn); CHECK_CONTIG(A); CHECK_CONTIG(B);
   CHECK_DT(sfa, at::kInt); CHECK_DT(sfb, at::kInt);
   const int M = A.size(0), K = A.size(1);
@@ -212,12 +212,14 @@ void gemm_fp8(torch::Tensor A, torch::Tensor sfa, torch::Tensor B, torch::Tensor
   const bool pair_path = epi != cb::GEMM_OUT_F32 && (pair == 1 || (pair < 0 && !grouped && M >= 512));
   const int splits = pair_path ? 1 : cb::gemm_fp8_splits(M, N, K, grouped, int(epi), num_sms());
   if (splits > 1) work = torch::empty({int64_t(splits) * M * N}, A.options().dtype(at::kFloat));
+  if (pair == 2 && grouped && epi == cb::GEMM_OUT_SWIGLU_FP8)
+    work = torch::empty({int64_t(M) * N}, A.options().dtype(at::kFloat));
   CK(cb::gemm_fp8(A.data_ptr(), B.data_ptr(), reinterpret_cast<uint32_t*>(sfa.data_ptr()),
                   reinterpret_cast<uint32_t*>(sfb.data_ptr()), M, N, K, Nb, out.data_ptr(), out.stride(0), epi,
                   ptr_or_null<uint32_t>(out_sf), float(swiglu_limit), ptr_or_null<const int>(m_block_expert),
                   ptr_or_null<const int>(num_m_blocks), grouped ? m_block_expert->numel() : 0,
                   ptr_or_null<int>(status), num_sms(), cur_stream(), int(pair),
-                  splits > 1 ? work.data_ptr<float>() : nullptr));
+                  work.defined() ? work.data_ptr<float>() : nullptr, ptr_or_null<const int>(row_valid)));
 }
 
 void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor out, int64_t epi,
@@ -245,7 +247,7 @@ void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor out, int64_t epi,
 // q [T, H, 192], kvb [T, H, 256] (k_nope | v), kpe [T, 64] -> out [T, H, 128]
 void attn_prefill(torch::Tensor q, torch::Tensor kvb, torch::Tensor kpe, torch::Tensor tiles,
                   c10::optional<torch::Tensor> mask, double scale, torch::Tensor out,
-                  c10::optional<torch::Tensor> status, int64_t version) {
+                  c10::optional<torch::Tensor> status, int64_t version, c10::optional<torch::Tensor> trace) {
   CHECK_CUDA(q); CHECK_DT(q, at::kBFloat16); CHECK_DT(kvb, at::kBFloat16); CHECK_DT(kpe, at::kBFloat16);
   CHECK_CONTIG(q); CHECK_CONTIG(kvb); CHECK_CONTIG(kpe); CHECK_CONTIG(out); CHECK_DT(tiles, at::kInt);
   TORCH_CHECK(q.size(2) == 192 && kvb.size(2) == 256 && kpe.size(-1) == 64, "attn_prefill: MLA dims 192/128");
@@ -255,10 +257,22 @@ void attn_prefill(torch::Tensor q, torch::Tensor kvb, torch::Tensor kpe, torch::
   int words = 0;
   if (mask.has_value()) { CHECK_DT((*mask), at::kInt); TORCH_CHECK(mask->size(0) == T); words = mask->size(1); }
   c10::cuda::CUDAGuard g(q.device());
-  auto fn = version == 2 ? cb::attn_prefill2 : cb::attn_prefill;
-  CK(fn(q.data_ptr(), kvb.data_ptr(), kpe.data_ptr(), T, H, tiles.data_ptr<int>(), tiles.size(0),
-        ptr_or_null<const uint32_t>(mask), words, float(scale), out.data_ptr(), ptr_or_null<int>(status),
-        cur_stream()));
+  if (version == 2) {
+    int64_t* tr = nullptr;
+    int cap = 0;
+    if (trace.has_value() && trace->defined()) {
+      TORCH_CHECK(trace->scalar_type() == at::kLong && trace->is_contiguous() && trace->numel() >= 3);
+      tr = trace->data_ptr<int64_t>();
+      cap = int((trace->numel() - 1) / 2);
+    }
+    CK(cb::attn_prefill2(q.data_ptr(), kvb.data_ptr(), kpe.data_ptr(), T, H, tiles.data_ptr<int>(), tiles.size(0),
+                         ptr_or_null<const uint32_t>(mask), words, float(scale), out.data_ptr(),
+                         ptr_or_null<int>(status), cur_stream(), tr, cap));
+  } else {
+    CK(cb::attn_prefill(q.data_ptr(), kvb.data_ptr(), kpe.data_ptr(), T, H, tiles.data_ptr<int>(), tiles.size(0),
+                        ptr_or_null<const uint32_t>(mask), words, float(scale), out.data_ptr(),
+                        ptr_or_null<int>(status), cur_stream()));
+  }
 }
 
 // keys [L, Di] bf16, q [Tq, H, Di] bf16, w [Tq, H] fp32 -> logits [Tq, ldo] fp32

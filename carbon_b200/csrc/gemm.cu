@@ -128,12 +128,15 @@ __global__ void splitk_reduce_out_kernel(const float* __restrict__ part, int spl
 // exactly the SwiGLU epilogue's arithmetic.  One warp per (row, 128 output columns), 4 outputs per lane.
 __global__ void splitk_reduce_swiglu_kernel(const float* __restrict__ part, int splits, int M, int N, float limit,
                                             uint8_t* __restrict__ out, int ldo, uint32_t* __restrict__ out_sf,
-                                            int sf_row_blocks) {
+                                            int sf_row_blocks, const int* __restrict__ row_valid,
+                                            const int* __restrict__ n_blocks) {
   const int I = N / 2, chunks = I / 128;
   const int wg = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (wg >= M * chunks) return;
   const int row = wg / chunks, g = wg % chunks;
+  if (n_blocks && row >= n_blocks[0] * 128) return;
+  if (row_valid && row_valid[row] < 0) return;     // padding rows of an expert segment: never read back
   float a[4];
   float amax = 0.f;
 #pragma unroll
@@ -204,7 +207,7 @@ static cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const Ge
 cudaError_t gemm_fp8(const void* A, const void* B, const uint32_t* sfa, const uint32_t* sfb, int M, int N, int K,
                      int Nb, void* out, int ldo, int epi, uint32_t* out_sf, float swiglu_limit,
                      const int* m_block_expert, const int* num_m_blocks_dev, int max_m_blocks, int* status,
-                     int num_sms, cudaStream_t s, int pair, float* work) {
+                     int num_sms, cudaStream_t s, int pair, float* work, const int* row_valid) {
   if (M <= 0 || N <= 0) return cudaSuccess;
   if (K % 128 || N % 16) return cudaErrorInvalidValue;
   // pair-tile kernel: dense prefill-sized GEMMs, and grouped GEMMs whose expert segments are 256-row aligned
@@ -231,6 +234,36 @@ cudaError_t gemm_fp8(const void* A, const void* B, const uint32_t* sfa, const ui
       return launch_pair<KIND_MXF8, EPI_SWIGLU_FP8, 2, 6>(ta, tb, tsa, tsb, p, units, num_sms, s);
     return launch_pair<KIND_MXF8, EPI_BF16, 2, 6>(ta, tb, tsa, tsb, p, units, num_sms, s);
   }
+  if (pair == 2 && m_block_expert) {
+    // decode-sized grouped GEMM (a few rows per expert): pure weight streaming.  The double-buffered 128-wide fp32
+    // kernel streams best; a SwiGLU output is then formed by a row-wise pass.  Padding rows are never written.
+    if (epi == GEMM_OUT_SWIGLU_FP8 && (!work || N % 256)) return cudaErrorInvalidValue;
+    CUtensorMap ta, tb;
+    if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, K, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+        !make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, Nb, K, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B))
+      return cudaErrorInvalidValue;
+    GemmParams p{};
+    p.M = M; p.N = N; p.K = K;
+    p.sfa = sfa; p.sfb = sfb;
+    p.sfa_row_blocks = ceil_div(M, 128);
+    p.sfb_row_blocks = ceil_div(Nb, 128);
+    p.m_block_expert = m_block_expert; p.num_m_blocks_dev = num_m_blocks_dev; p.status = status;
+    p.row_valid = row_valid;
+    const int max_tiles = max_m_blocks * ceil_div(N, 128);
+    if (epi == GEMM_OUT_SWIGLU_FP8) {
+      p.out = work; p.ldo = N;
+      cudaError_t e = launch<KIND_MXF8, EPI_F32, 128, 6, 2>(ta, tb, p, max_tiles, num_sms, s);
+      if (e != cudaSuccess) return e;
+      const int warps = M * (N / 256);
+      splitk_reduce_swiglu_kernel<<<ceil_div(warps, 8), 256, 0, s>>>(work, 1, M, N, swiglu_limit,
+                                                                     reinterpret_cast<uint8_t*>(out), ldo, out_sf,
+                                                                     ceil_div(M, 128), row_valid, num_m_blocks_dev);
+      return cudaGetLastError();
+    }
+    p.out = out; p.ldo = ldo;
+    if (epi == GEMM_OUT_F32) return launch<KIND_MXF8, EPI_F32, 128, 6, 2>(ta, tb, p, max_tiles, num_sms, s);
+    return launch<KIND_MXF8, EPI_BF16, 128, 6, 2>(ta, tb, p, max_tiles, num_sms, s);
+  }
   const int splits = work ? gemm_fp8_splits(M, N, K, m_block_expert != nullptr, epi, num_sms) : 1;
   if (splits > 1) {
     // partial slabs of K ranges (fp32, one 128x128 tile per CTA), then an ordered reduction into the output
@@ -254,7 +287,7 @@ cudaError_t gemm_fp8(const void* A, const void* B, const uint32_t* sfa, const ui
       const int warps = M * (N / 256);
       splitk_reduce_swiglu_kernel<<<ceil_div(warps, 8), 256, 0, s>>>(work, used, M, N, swiglu_limit,
                                                                      reinterpret_cast<uint8_t*>(out), ldo, out_sf,
-                                                                     ceil_div(M, 128));
+                                                                     ceil_div(M, 128), nullptr, nullptr);
     } else {
       const int64_t total4 = int64_t(M) * (N / 4);
       const int blocks = int(total4 / 256 + 1 < 1024 ? total4 / 256 + 1 : 1024);

@@ -48,6 +48,8 @@ struct GemmParams {
   const uint64_t* scatter_ptrs;
   const int* scatter_bounds;
   int scatter_world, scatter_rank, scatter_rows;
+  // optional: rows with row_valid[row] < 0 (expert-segment padding) are not written by the epilogue
+  const int* row_valid;
 };
 
 template <int BLOCK_N>
@@ -236,7 +238,7 @@ __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__
       if (!mbar_wait(&tfull_bar[acc], acc_phase)) { fail(kErrTimeoutTmem); break; }
       tc_fence_after();
       const int row = mb * BLOCK_M + row_in_tile;
-      const bool row_ok = row < p.M;
+      const bool row_ok = row < p.M && (p.row_valid == nullptr || p.row_valid[row] >= 0);
       const uint32_t t_row = tmem_base + ((q * 32) << 16) + acc * BLOCK_N;
       if constexpr (EPI == EPI_BF16 || EPI == EPI_F32 || EPI == EPI_BF16_SCATTER) {
         __nv_bfloat16* row_base = nullptr;

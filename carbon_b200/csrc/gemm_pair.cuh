@@ -294,7 +294,7 @@ __global__ void __launch_bounds__(PairCfg<KIND, PAIR, EPI>::kThreads, 1)
       if (!mbar_wait(&tfull_bar[s], (j >> 1) & 1)) { fail(kErrTimeoutTmem); break; }
       tc_fence_after();
       const int row = mb * BM + int(rank) * 128 + row_in_cta;
-      const bool row_ok = row < p.M;
+      const bool row_ok = row < p.M && (p.row_valid == nullptr || p.row_valid[row] >= 0);
       const uint32_t t_row = tmem_base + ((q * 32) << 16) + (s ? C::kAcc1 : C::kAcc0);
       // the warp that owns this stage's overlap columns drains them first
       const bool ovl_first = C::kOvl > 0 && s == 0 && h == 1;       // stage 0: local columns [224,256)

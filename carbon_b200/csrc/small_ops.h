@@ -42,7 +42,8 @@ enum GemmEpiHost { GEMM_OUT_BF16 = 0, GEMM_OUT_SWIGLU_FP8 = 1, GEMM_OUT_F32 = 2 
 cudaError_t gemm_fp8(const void* A, const void* B, const uint32_t* sfa, const uint32_t* sfb, int M, int N, int K,
                      int Nb, void* out, int ldo, int epi, uint32_t* out_sf, float swiglu_limit,
                      const int* m_block_expert, const int* num_m_blocks_dev, int max_m_blocks, int* status,
-                     int num_sms, cudaStream_t s, int pair = -1, float* work = nullptr);
+                     int num_sms, cudaStream_t s, int pair = -1, float* work = nullptr,
+                     const int* row_valid = nullptr);
 // K splits gemm_fp8 uses for a dense small-M GEMM (work must then hold splits * M * N floats).
 int gemm_fp8_splits(int M, int N, int K, bool grouped, int epi, int num_sms);
 cudaError_t gemm_bf16(const void* A, int lda, const void* B, int ldb, int M, int N, int K, int Nb, void* out, int ldo,
@@ -54,9 +55,10 @@ cudaError_t attn_prefill(const void* q, const void* kvb, const void* kpe, int T,
                          int n_tiles, const uint32_t* mask, int mask_words, float scale, void* out, int* status,
                          cudaStream_t s);
 
+// trace (optional, int64 [1 + 2*trace_cap], zeroed): event timeline of CTA (0,0), see attn_prefill.cu
 cudaError_t attn_prefill2(const void* q, const void* kvb, const void* kpe, int T, int H, const int* tiles,
                           int n_tiles, const uint32_t* mask, int mask_words, float scale, void* out, int* status,
-                          cudaStream_t s);
+                          cudaStream_t s, int64_t* trace = nullptr, int trace_cap = 0);
 
 // DSA indexer: logits GEMM with fused relu/weight/head-sum epilogue (gemm.cu) and exact top-k bitmask (topk.cu)
 cudaError_t indexer_logits(const void* keys, int L, const void* q, int Tq, int H, int Di, const float* w, float* out,

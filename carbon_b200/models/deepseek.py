@@ -449,10 +449,10 @@ class DeepseekModel:
         I2 = 2 * cfg.moe_intermediate
         with region("moe.gemm_up"):
             act, act_sf = fp8_gemm_swiglu(a_q, a_sf, L.e_w13, cfg.swiglu_limit, lay.m_block_expert, lay.num_blocks,
-                                          I2, pair=lay.pair)
+                                          I2, pair=lay.pair, row_valid=lay.row_src)
         with region("moe.gemm_down"):
             y = fp8_gemm(act, act_sf, L.e_w2, m_block_expert=lay.m_block_expert, num_m_blocks=lay.num_blocks,
-                         n_per_group=cfg.hidden_size, pair=lay.pair)
+                         n_per_group=cfg.hidden_size, pair=lay.pair, row_valid=lay.row_src)
         with region("moe.combine"):
             return C.moe_combine(y, w, lay.slot_pos, resolve(shared), T)
 

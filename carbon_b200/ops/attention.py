@@ -24,14 +24,14 @@ from ._ext import ext
 
 
 def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens: List[int], scale: float,
-                      key_masks=None, version: int = 2) -> torch.Tensor:
+                      key_masks=None, version: int = 2, trace: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Reference-layout entry: q [T,H,dqk], k [T,H,dqk], v [T,H,dv]."""
     T, H, dv = q.shape[0], q.shape[1], v.shape[2]
     if q.is_cuda and q.shape[2] == 192 and dv == 128:
         dn = 128
         kvb = torch.cat([k[..., :dn], v], dim=-1).contiguous()
         kpe = k[:, 0, dn:].contiguous()
-        return mla_prefill(q, kvb, kpe, cu_seqlens, scale, key_masks, version)
+        return mla_prefill(q, kvb, kpe, cu_seqlens, scale, key_masks, version, trace)
     out = torch.empty(T, H, dv, dtype=torch.float32, device=q.device)
     if isinstance(key_masks, torch.Tensor):
         key_masks = unpack_key_mask(key_masks, cu_seqlens)
@@ -44,7 +44,7 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seql
 
 
 def mla_prefill(q: torch.Tensor, kvb: torch.Tensor, kpe: torch.Tensor, cu_seqlens: List[int], scale: float,
-                key_masks=None, version: int = 2) -> torch.Tensor:
+                key_masks=None, version: int = 2, trace: Optional[torch.Tensor] = None) -> torch.Tensor:
     """MLA prefill in the projection's own layout: q [T,H,192], kvb [T,H,256] = (k_nope | v) straight from the
     wkv_b GEMM, kpe [T,64] the shared RoPE key (k = [k_nope, kpe] per head). Returns o [T,H,128].
     version 2: two 128-row Q tiles per CTA sharing each K/V tile (the default); 1: one Q tile per CTA."""
@@ -61,7 +61,7 @@ def mla_prefill(q: torch.Tensor, kvb: torch.Tensor, kpe: torch.Tensor, cu_seqlen
     out = torch.empty(T, H, 128, dtype=torch.bfloat16, device=q.device)
     tiles = prefill_tiles(cu_seqlens, 256 if version == 2 else 128).to(q.device, non_blocking=True)
     ext().attn_prefill(q.contiguous(), kvb.contiguous(), kpe.contiguous(), tiles, mask, float(scale), out, None,
-                       version)
+                       version, trace)
     return out
 
 

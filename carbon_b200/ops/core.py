@@ -141,8 +141,11 @@ class MoeLayout:
 
     @property
     def pair(self) -> int:
-        """GEMM tile mode for this layout (1 = CTA-pair tiles, 0 = 128-row tiles)."""
-        return 1 if self.align == 256 else 0
+        """GEMM tile mode for this layout: 1 = CTA-pair tiles, 2 = weight streaming (a few rows per expert, decode),
+        0 = 128-row tiles."""
+        if self.align == 256:
+            return 1
+        return 2 if self.T * self.k <= 32 * self.E else 0
 
 
 def moe_combine(Y: torch.Tensor, w: torch.Tensor, slot_pos: torch.Tensor, add: Optional[torch.Tensor],

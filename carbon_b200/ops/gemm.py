@@ -24,9 +24,10 @@ OUT_BF16, OUT_SWIGLU_FP8, OUT_F32 = 0, 1, 2
 
 def fp8_gemm(a_q: torch.Tensor, a_sf: torch.Tensor, w: Fp8Weight, out_dtype=torch.bfloat16,
              out: Optional[torch.Tensor] = None, m_block_expert=None, num_m_blocks=None, n_per_group: int = 0,
-             status=None, pair: int = -1) -> torch.Tensor:
+             status=None, pair: int = -1, row_valid=None) -> torch.Tensor:
     """pair: -1 = automatic (256x256 CTA-pair tiles for dense GEMMs with >= 512 rows), 1 = pair tiles (a grouped
-    layout must then pad expert segments to 256 rows), 0 = 128-row tiles."""
+    layout must then pad expert segments to 256 rows), 0 = 128-row tiles, 2 = weight streaming for grouped GEMMs
+    with a few rows per expert (decode).  row_valid: rows < 0 are padding and are not written."""
     M = a_q.shape[0]
     N = n_per_group if m_block_expert is not None else w.q.shape[0]
     if not a_q.is_cuda:
@@ -36,12 +37,12 @@ def fp8_gemm(a_q: torch.Tensor, a_sf: torch.Tensor, w: Fp8Weight, out_dtype=torc
         out = torch.empty(M, N, dtype=out_dtype, device=a_q.device)
     epi = OUT_F32 if out.dtype == torch.float32 else OUT_BF16
     ext().gemm_fp8(a_q, a_sf, w.q, w.sf, out, epi, None, 0.0, m_block_expert, num_m_blocks, n_per_group, status,
-                   pair)
+                   pair, row_valid)
     return out
 
 
 def fp8_gemm_swiglu(a_q, a_sf, w13: Fp8Weight, limit: float = 0.0, m_block_expert=None, num_m_blocks=None,
-                    n_per_group: int = 0, status=None, pair: int = -1):
+                    n_per_group: int = 0, status=None, pair: int = -1, row_valid=None):
     """w13 rows are interleaved in 128-row chunks: [gate 0:128, up 0:128, gate 128:256, up 128:256, ...].
     Returns (act fp8 [M, N/2], act SF tiles)."""
     M = a_q.shape[0]
@@ -49,7 +50,7 @@ def fp8_gemm_swiglu(a_q, a_sf, w13: Fp8Weight, limit: float = 0.0, m_block_exper
     out = torch.empty(M, N // 2, dtype=torch.float8_e4m3fn, device=a_q.device)
     out_sf = empty_sf(M, N // 2, a_q.device)
     ext().gemm_fp8(a_q, a_sf, w13.q, w13.sf, out, OUT_SWIGLU_FP8, out_sf, float(limit), m_block_expert, num_m_blocks,
-                   n_per_group, status, pair)
+                   n_per_group, status, pair, row_valid)
     return out, out_sf
 
 
