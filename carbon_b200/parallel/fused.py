@@ -157,7 +157,9 @@ class FusedCtx(DistCtx):
         ext().embed_peer(b.peers, per, ids, X, sumsq)
         return X, sumsq
 
-    def _moe_bufs(self, model, T_l: int):
+    def _moe_bufs(self, model, T_l: int, chunk: int = 0):
+        """Heap buffers of one MoE chunk: set 0 holds a whole call (max_local tokens), set 1 the second half of a
+        two-chunk call."""
         cfg = model.cfg
         D, El, k = cfg.hidden_size, model.E_local, cfg.n_activated_experts
         from ..ops.core import moe_align
@@ -165,11 +167,14 @@ class FusedCtx(DistCtx):
         # expert segments of the owner's buffer are padded to 256 rows (CTA-pair GEMM tiles) when experts average
         # enough rows; the choice depends only on static sizes, so every rank makes the same one
         align = moe_align(self.max_local * k * self.world, El * self.world)
-        cap = int(self.max_local * k * self.moe_capacity) + El * align
+        tokens = self.max_local if chunk == 0 else (self.max_local + 1) // 2
+        cap = int(tokens * k * self.moe_capacity) + El * align
         cap = (cap + 255) // 256 * 256
-        if self._moe is None or self._moe["align"] != align:
+        if self._moe is None:
+            self._moe = [None, None]
+        if self._moe[chunk] is None or self._moe[chunk]["align"] != align:
             h = self.heap
-            self._moe = {
+            self._moe[chunk] = {
                 "cnt": h.alloc((self.world, El), torch.int32),
                 "off": h.alloc((self.world, El), torch.int32),
                 "recv": h.alloc((cap, D), torch.float8_e4m3fn),
@@ -180,42 +185,99 @@ class FusedCtx(DistCtx):
                 "nb": torch.empty(1, dtype=torch.int32, device=self.device),
                 "align": align,
             }
-        return self._moe
+        return self._moe[chunk]
+
+    # a call is split in two pipelined chunks once the whole batch has at least this many tokens per rank
+    CHUNK_MIN_TOKENS_PER_RANK = 2048
 
     def moe(self, model, L, h, w, ids, shared, hq=None):
+        """EP MoE over NVLink.  Prefill-sized calls run as two token chunks on a communication stream and the
+        compute stream: chunk 1's dispatch overlaps chunk 0's expert GEMMs, chunk 0's combine overlaps chunk 1's.
+        Every cross-rank barrier is issued on the communication stream, in the same order on every rank."""
         cfg = model.cfg
-        e = ext()
         T, k = ids.shape
-        El, E = model.E_local, cfg.n_routed_experts
-        m = self._moe_bufs(model, T)
         ids = ids.to(torch.int32).contiguous()
+        wf = w.float().contiguous()
         from ..models.deepseek import resolve
         from ..utils.trace import region
 
-        with region("moe.dispatch"):
-            pair_rank = torch.empty(T * k, dtype=torch.int32, device=h.device)
-            e.moe_count(ids.view(-1), E, self.rank, m["cnt"].peers, pair_rank)
-            self.barrier()
-            e.moe_owner_layout(m["cnt"].local, self.world, El, m["off"].local, m["mbe"], m["nb"], m["align"])
-            self.barrier()
-            pos = torch.empty(T, k, dtype=torch.int32, device=h.device)
+        total = self.bounds[-1] - self.bounds[0] if self.bounds is not None else T
+        chunked = total >= self.CHUNK_MIN_TOKENS_PER_RANK * self.world and self.device.type == "cuda"
+        out = torch.empty(T, cfg.hidden_size, dtype=torch.bfloat16, device=h.device)
+        if not chunked:
+            m = self._moe_bufs(model, T, 0)
+            with region("moe.dispatch"):
+                pos = self._moe_dispatch(model, m, h, ids)
+            self._moe_gemms(model, L, m)
+            with region("moe.combine"):
+                self.barrier()
+                ext().moe_combine_pull(m["y"].peers, ids, pos, wf, model.E_local, resolve(shared), out)
+                self.barrier()     # peers may not reuse `y` until every rank has pulled its rows
+            return out
+        main = torch.cuda.current_stream()
+        if getattr(self, "_comm", None) is None:
+            self._comm = torch.cuda.Stream(device=self.device)
+        cs = self._comm
+        half = (T + 1) // 2
+        spans = [(0, half), (half, T)]
+        bufs = [self._moe_bufs(model, T, c) for c in range(2)]
+        ev_disp = [torch.cuda.Event() for _ in range(2)]
+        ev_gemm = [torch.cuda.Event() for _ in range(2)]
+        poss = [None, None]
+        for t_ in (h, ids, wf, out):
+            t_.record_stream(cs)
+        cs.wait_stream(main)
+        with torch.cuda.stream(cs), region("moe.dispatch"):
+            for c, (a, b) in enumerate(spans):
+                poss[c] = self._moe_dispatch(model, bufs[c], h[a:b], ids[a:b])
+                ev_disp[c].record(cs)
+        for c in range(2):
+            main.wait_event(ev_disp[c])
+            self._moe_gemms(model, L, bufs[c])
+            ev_gemm[c].record(main)
+        with torch.cuda.stream(cs), region("moe.combine"):
+            sh = resolve(shared)
+            for c, (a, b) in enumerate(spans):
+                cs.wait_event(ev_gemm[c])
+                self.barrier()
+                if b > a:
+                    ext().moe_combine_pull(bufs[c]["y"].peers, ids[a:b], poss[c], wf[a:b], model.E_local,
+                                           sh[a:b] if sh is not None else None, out[a:b])
+            self.barrier()         # peers may not reuse `y` until every rank has pulled its rows
+        main.wait_stream(cs)
+        return out
+
+    def _moe_dispatch(self, model, m, h, ids):
+        """Count -> owner layout -> quantise + P2P row stores into the owners' expert-sorted buffers."""
+        e = ext()
+        cfg = model.cfg
+        T, k = ids.shape
+        El, E = model.E_local, cfg.n_routed_experts
+        pair_rank = torch.empty(max(T * k, 1), dtype=torch.int32, device=self.device)
+        e.moe_count(ids.reshape(-1), E, self.rank, m["cnt"].peers, pair_rank)
+        self.barrier()
+        e.moe_owner_layout(m["cnt"].local, self.world, El, m["off"].local, m["mbe"], m["nb"], m["align"])
+        self.barrier()
+        pos = torch.empty(T, k, dtype=torch.int32, device=self.device)
+        if T > 0:
             e.moe_dispatch(h.contiguous(), ids, El, self.rank, pair_rank, m["recv"].peers, m["sf"].peers,
                            m["off"].peers, m["cap"], pos, self.status)
-            self.barrier()
-        # owner: grouped GEMMs over the expert-sorted received rows, in place in the heap
+        self.barrier()
+        return pos
+
+    def _moe_gemms(self, model, L, m):
+        """Owner side: grouped GEMMs over the expert-sorted received rows, in place in the heap."""
+        from ..utils.trace import region
+
+        cfg = model.cfg
         I2 = 2 * cfg.moe_intermediate
+        mode = int(m["align"] == 256)
         with region("moe.gemm_up"):
             act, act_sf = fp8_gemm_swiglu(m["recv"].local, m["sf"].local, L.e_w13, cfg.swiglu_limit, m["mbe"],
-                                          m["nb"], I2, pair=int(m["align"] == 256))
+                                          m["nb"], I2, pair=mode)
         with region("moe.gemm_down"):
             fp8_gemm(act, act_sf, L.e_w2, out=m["y"].local, m_block_expert=m["mbe"], num_m_blocks=m["nb"],
-                     n_per_group=cfg.hidden_size, pair=int(m["align"] == 256))
-        with region("moe.combine"):
-            self.barrier()
-            out = torch.empty(T, cfg.hidden_size, dtype=torch.bfloat16, device=h.device)
-            e.moe_combine_pull(m["y"].peers, ids, pos, w.float().contiguous(), El, resolve(shared), out)
-            self.barrier()     # peers may not reuse `y` until every rank has pulled its rows
-        return out
+                     n_per_group=cfg.hidden_size, pair=mode)
 
     def lm_head(self, model, y: torch.Tensor) -> torch.Tensor:
         part = model.head_w(y, out_dtype=torch.float32)                     # [n, V/world]
