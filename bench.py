@@ -48,6 +48,9 @@ def parse():
     ap.add_argument("--profile", action="store_true", help="print per-region device times (stderr)")
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                     help="multi-GPU data movement: our NVLink kernels (fused) or the NCCL baseline")
+    ap.add_argument("--attn", default="tp", choices=["tp", "dp"],
+                    help="attention parallelism for N>1: tensor-parallel over heads (the BASELINE config) or "
+                         "data-parallel over each rank's own sequences")
     return ap.parse_args()
 
 
@@ -155,13 +158,13 @@ def main():
     elif args.comm == "nccl":
         from carbon_b200.parallel.dist import DistCtx
 
-        pctx = DistCtx(rank, world)
+        pctx = DistCtx(rank, world, attn_dp=args.attn == "dp")
     else:
         from carbon_b200.parallel.fused import FusedCtx
 
         max_tokens = max(P * S, B) * world
         pctx = FusedCtx(rank, world, heap_bytes=heap_bytes(cfg, world, max_tokens, S), max_tokens=max_tokens,
-                        max_seq=S)
+                        max_seq=S, attn_dp=args.attn == "dp")
     mem = torch.cuda.get_device_properties(dev).total_memory
     page = 64
     dec_pages = (B * world) * ((ctx + args.decode_steps * (args.warmup + args.steps) * 2 + 2 * page) // page + 1)
@@ -310,7 +313,8 @@ def pctx_name(p, world):
     if world == 1:
         return "single GPU"
     kind = "NVLink peer-memory kernels" if type(p).__name__ == "FusedCtx" else "NCCL baseline"
-    return f"tp{p.tp} attention + ep{p.ep} MoE, sequence-sharded residual ({kind})"
+    attn = f"dp{world} attention" if getattr(p, "attn_dp", False) else f"tp{p.tp} attention"
+    return f"{attn} + ep{p.ep} MoE, sequence-sharded residual ({kind})"
 
 
 def heap_bytes(cfg, world, max_tokens, max_seq):

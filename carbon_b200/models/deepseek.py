@@ -296,6 +296,7 @@ class DeepseekModel:
         dn, dr, dv, r = cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.v_head_dim, cfg.kv_lora_rank
         lo, hi = pc.local
         pos_l = fb.pos[lo:hi]
+        dp = pc.attn_dp and pc.world > 1         # attention over this rank's own sequences, all heads
         with region("attn.q_proj"):
             if cfg.q_lora_rank > 0:
                 q_lat_raw = L.wq_a(h, xq=hq)
@@ -314,14 +315,21 @@ class DeepseekModel:
         if cfg.use_indexer:
             with region("attn.indexer_qk"):
                 idx_l = self.indexer_qkw(i, h, q_lat_l, pos_l)
-        with region("tp.gather"):
-            q_lat = pc.gather_rows(q_lat_l.to(self.act_dtype) if self.on_gpu else q_lat_l)
-            latent = pc.gather_rows(latent_l)
-            idx_k = pc.gather_rows(idx_l[1]) if idx_l is not None else None
+        q_lat_a = q_lat_l.to(self.act_dtype) if self.on_gpu else q_lat_l
+        if dp:
+            q_lat, latent = q_lat_a, latent_l
+            idx_k = idx_l[1] if idx_l is not None else None
+            out_loc = fb.out_loc[lo:hi]
+        else:
+            with region("tp.gather"):
+                q_lat = pc.gather_rows(q_lat_a)
+                latent = pc.gather_rows(latent_l)
+                idx_k = pc.gather_rows(idx_l[1]) if idx_l is not None else None
+            out_loc = fb.out_loc
         with region("attn.kv_proj"):
-            cache.write_latent(i, fb.out_loc, latent)
+            cache.write_latent(i, out_loc, latent)
             if idx_k is not None:
-                cache.write_index_k(i, fb.out_loc, idx_k)
+                cache.write_index_k(i, out_loc, idx_k)
         T = q_lat.shape[0]
         with region("attn.q_proj"):
             if cfg.q_lora_rank > 0:
@@ -330,13 +338,14 @@ class DeepseekModel:
                 q = L.wq(q_lat).view(T, Hl, dn + dr)
             if not self.on_gpu:
                 q = q.clone()
-            C.rope_(q, dn, dr, self.cos_sin, fb.pos)
+            C.rope_(q, dn, dr, self.cos_sin, pos_l if dp else fb.pos)
         if fb.is_prefill:
-            o = self._attn_prefill(i, q, latent, fb, idx_l, cache)
+            o = self._attn_prefill(i, q, latent, fb, idx_l, cache, dp)
         else:
-            o = self._attn_decode(i, q, fb, cache, idx_l)
+            o = self._attn_decode(i, q, fb, cache, idx_l, dp)
         with region("attn.o_proj"):
-            return pc.row_parallel_out(L.wo, o.reshape(T, Hl * dv).to(self.act_dtype).contiguous())
+            o2 = o.reshape(T, Hl * dv).to(self.act_dtype).contiguous()
+            return L.wo(o2) if dp else pc.row_parallel_out(L.wo, o2)
 
     def indexer_qkw(self, i, h, q_lat, pos):
         cfg, L = self.cfg, self.layers[i]
@@ -351,8 +360,9 @@ class DeepseekModel:
         w = (L.idx_wp(h, out_dtype=torch.float32) * (Hi ** -0.5) * (Di ** -0.5)).float()
         return q, k.view(T, Di), w
 
-    def _prefill_key_masks(self, idx_l, fb: ForwardBatch):
-        """DSA selection of this rank's sequences, gathered to all ranks (rows in global token order)."""
+    def _prefill_key_masks(self, idx_l, fb: ForwardBatch, gather: bool = True):
+        """DSA selection of this rank's sequences, gathered to all ranks (rows in global token order) unless the
+        attention is data-parallel (then only this rank's rows are needed)."""
         pc = self.pctx
         lo, hi = pc.local
         cu_l = [c - lo for c in fb.cu_seqlens if lo <= c <= hi]
@@ -361,34 +371,40 @@ class DeepseekModel:
             return None
         q, k, w = idx_l
         m = A.indexer_prefill_mask(q, k, w, cu_l if len(cu_l) > 1 else [0, 0], self.cfg.index_topk, lmax=lmax)
-        return pc.gather_rows(m)
+        return pc.gather_rows(m) if gather else m
 
-    def _attn_prefill(self, i, q, latent, fb, idx_l, cache):
-        cfg, L = self.cfg, self.layers[i]
+    def _attn_prefill(self, i, q, latent, fb, idx_l, cache, dp: bool = False):
+        cfg, L, pc = self.cfg, self.layers[i], self.pctx
         T, Hl = q.shape[0], self.H_local
         dn, dr, dv, r = cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.v_head_dim, cfg.kv_lora_rank
+        cu = fb.cu_seqlens
+        if dp:
+            lo, hi = pc.local
+            cu = [c - lo for c in fb.cu_seqlens if lo <= c <= hi]
+            if len(cu) < 2:
+                cu = [0, 0]
         with region("attn.kv_up"):
             kvb = L.wkv_b(latent[:, :r].contiguous()).view(T, Hl, dn + dv)
         with region("attn.indexer_topk"):
-            masks = self._prefill_key_masks(idx_l, fb) if idx_l is not None else None
+            masks = self._prefill_key_masks(idx_l, fb, gather=not dp) if idx_l is not None else None
         with region("attn.core_prefill"):
-            return A.mla_prefill(q, kvb, latent[:, r:].contiguous(), fb.cu_seqlens, cfg.softmax_scale, masks)
+            return A.mla_prefill(q, kvb, latent[:, r:].contiguous(), cu, cfg.softmax_scale, masks)
 
-    def _attn_decode(self, i, q, fb, cache, idx_l):
+    def _attn_decode(self, i, q, fb, cache, idx_l, dp: bool = False):
         cfg, L, pc = self.cfg, self.layers[i], self.pctx
         T, Hl = q.shape[0], self.H_local
         dn, r = cfg.qk_nope_head_dim, cfg.kv_lora_rank
+        lo, hi = pc.local
         with region("attn.absorb_q"):
             q_abs = head_bmm(q[..., :dn], L.w_uk)                                    # [T, Hl, r]
             qf = torch.cat([q_abs.to(self.act_dtype), q[..., dn:].to(self.act_dtype)], dim=-1).contiguous()
-        idx = fb.key_slots
+        idx = fb.key_slots[lo:hi] if dp else fb.key_slots
         if idx_l is not None and int(fb.key_slots.shape[1]) > cfg.index_topk:
             with region("attn.indexer_topk"):
-                lo, hi = pc.local
                 qi, _, wi = idx_l
                 sel = A.indexer_topk(qi, wi, cache.index_k[i], fb.key_slots[lo:hi].contiguous(),
                                      fb.n_keys[lo:hi].contiguous(), cfg.index_topk)
-                idx = pc.gather_rows(sel)
+                idx = sel if dp else pc.gather_rows(sel)
         with region("attn.core_decode"):
             o_lat = A.sparse_mla(qf, cache.latent[i], idx.contiguous(), cfg.softmax_scale, r)   # [T, Hl, r]
         with region("attn.absorb_o"):

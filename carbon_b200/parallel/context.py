@@ -29,6 +29,9 @@ class ParallelCtx:
     tp_rank: int = 0
     ep_rank: int = 0
     vocab_parallel: bool = False
+    # DP attention: every rank runs attention for its own sequences with all heads (tp = 1 for attention weights,
+    # no attention collectives); MoE stays expert-parallel over all ranks
+    attn_dp: bool = False
     group: Optional[object] = None   # torch.distributed process group (NCCL) when world > 1
     bounds: Optional[list] = None    # token shard bounds of the current batch ([0, T] on one rank)
 

@@ -48,9 +48,12 @@ def split_bounds(lengths: List[int], world: int) -> List[int]:
 
 
 class DistCtx(ParallelCtx):
-    def __init__(self, rank: int, world: int, group=None):
-        super().__init__(rank=rank, world=world, tp=world, ep=world, tp_rank=rank, ep_rank=rank,
-                         vocab_parallel=True, group=group)
+    def __init__(self, rank: int, world: int, group=None, attn_dp: bool = False):
+        """attn_dp: data-parallel attention (each rank attends over its own sequences with all heads) instead of
+        tensor-parallel attention over heads; MoE is expert-parallel either way."""
+        super().__init__(rank=rank, world=world, tp=1 if attn_dp else world, ep=world,
+                         tp_rank=0 if attn_dp else rank, ep_rank=rank, vocab_parallel=True, attn_dp=attn_dp,
+                         group=group)
         self.bounds: Optional[List[int]] = None
 
     # -- shard bookkeeping ----------------------------------------------------------------------------------------

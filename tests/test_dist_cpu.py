@@ -1,5 +1,6 @@
-"""Multi-rank engine on CPU (gloo, 2 ranks): TP attention over heads, EP MoE over experts, vocab-parallel embedding
-and LM head, sequence-sharded residual.  Every rank's logits must equal the single-process engine's within 1e-4."""
+"""Multi-rank engine on CPU (gloo, 2 ranks): TP attention over heads (or DP attention over each rank's own
+sequences), EP MoE over experts, vocab-parallel embedding and LM head, sequence-sharded residual.  Every rank's
+logits must equal the single-process engine's within 1e-4."""
 import os
 import socket
 
@@ -27,7 +28,7 @@ def _prompts(cfg):
     return [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (64, 50, 70)]
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, attn_dp=False):
     from datetime import timedelta
 
     from carbon_b200.parallel.dist import DistCtx
@@ -39,15 +40,15 @@ def _worker(rank, world, port, q):
         cfg = tiny_config()
         w = init_weights(cfg, seed=0)
         eng = Engine(cfg, device="cpu", source=WeightSource(cfg, state=w), num_pages=32, page_size=16,
-                     pctx=DistCtx(rank, world))
+                     pctx=DistCtx(rank, world, attn_dp=attn_dp))
         outs, hist = eng.generate(_prompts(cfg), max_new_tokens=6, return_logits=True)
         q.put((rank, outs, [h.numpy().copy() for h in hist]))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2])
-def test_tp_ep_engine_matches_single_rank(world):
+@pytest.mark.parametrize("world,attn_dp", [(2, False), (2, True)])
+def test_tp_ep_engine_matches_single_rank(world, attn_dp):
     cfg = tiny_config()
     w = init_weights(cfg, seed=0)
     single = Engine(cfg, device="cpu", source=WeightSource(cfg, state=w), num_pages=32, page_size=16)
@@ -55,7 +56,7 @@ def test_tp_ep_engine_matches_single_rank(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, attn_dp)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=300) for _ in range(world)]

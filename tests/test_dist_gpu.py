@@ -50,7 +50,7 @@ def _run_forced(eng, prompts, steps=4):
     return hist
 
 
-def _worker(rank, world, port, comm, q):
+def _worker(rank, world, port, comm, q, attn_dp=False):
     from datetime import timedelta
 
     from carbon_b200.engine.engine import Engine
@@ -70,9 +70,9 @@ def _worker(rank, world, port, comm, q):
         cfg = _cfg()
         w = init_weights(cfg, seed=0)
         if comm == "fused":
-            pctx = FusedCtx(rank, world, heap_bytes=1 << 30, max_tokens=1024, max_seq=512)
+            pctx = FusedCtx(rank, world, heap_bytes=1 << 30, max_tokens=1024, max_seq=512, attn_dp=attn_dp)
         else:
-            pctx = DistCtx(rank, world)
+            pctx = DistCtx(rank, world, attn_dp=attn_dp)
         eng = Engine(cfg, device=dev, source=WeightSource(cfg, state=w), num_pages=64, page_size=64, pctx=pctx)
         hist = _run_forced(eng, _prompts(cfg))
         outs = []
@@ -90,8 +90,8 @@ def _worker(rank, world, port, comm, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("comm", ["fused", "nccl"])
-def test_two_gpu_engine_matches_single_gpu(comm):
+@pytest.mark.parametrize("comm,attn_dp", [("fused", False), ("nccl", False), ("fused", True), ("nccl", True)])
+def test_two_gpu_engine_matches_single_gpu(comm, attn_dp):
     from carbon_b200.engine.engine import Engine
     from carbon_b200.models.weights import WeightSource
     from carbon_b200.ref.model import init_weights
@@ -105,7 +105,7 @@ def test_two_gpu_engine_matches_single_gpu(comm):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, comm, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, comm, q, attn_dp)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=420) for _ in range(2)]
