@@ -133,7 +133,7 @@ def test_pair_grouped_swiglu_and_down_projection(T, align, mode):
             gu = (xd[t] @ W13[e].dequant().t()).view(-1, 2, 128)
             ref_act = R.swiglu(gu[:, 0].reshape(-1), gu[:, 1].reshape(-1))
             p = int(slot[t, j])
-            assert rel_err(act_d[p], ref_act) < 0.04
+            assert rel_err(act_d[p], ref_act) < 0.05      # fp8 e4m3 requantisation of the activations
             ref_y = act_d[p] @ W2[e].dequant().t()
             assert rel_err(y[p], ref_y) < 1e-2
 
