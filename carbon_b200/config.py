@@ -40,6 +40,12 @@ class ModelConfig:
     index_n_heads: int = 64
     index_head_dim: int = 128
     index_topk: int = 2048
+    # DSA selection sharing (DeepSeek-V4.1 style): when non-empty, only these layers run the indexer; every later
+    # layer reuses the selection of the most recent source layer; layers before the first source attend densely.
+    # Empty: every layer runs its own indexer.
+    index_sources: tuple = ()
+    # per-head learned attention sink: one extra logit in each softmax denominator (attn.sink [n_heads] fp32)
+    attn_sink: bool = False
     # MoE
     n_routed_experts: int = 256
     n_activated_experts: int = 8
@@ -70,6 +76,19 @@ class ModelConfig:
     @property
     def use_indexer(self) -> bool:
         return self.index_n_heads > 0 and self.index_topk > 0
+
+    def index_source(self, layer: int) -> Optional[int]:
+        """Layer whose DSA selection this layer's attention uses (None: dense attention)."""
+        if not self.use_indexer:
+            return None
+        if not self.index_sources:
+            return layer
+        srcs = [s for s in self.index_sources if s <= layer]
+        return max(srcs) if srcs else None
+
+    def has_indexer(self, layer: int) -> bool:
+        """Whether this layer holds indexer weights and writes indexer keys to the cache."""
+        return self.use_indexer and (not self.index_sources or layer in self.index_sources)
 
     def is_moe_layer(self, layer: int) -> bool:
         return layer >= self.n_dense_layers and self.n_routed_experts > 0

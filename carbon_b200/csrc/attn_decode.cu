@@ -41,6 +41,7 @@ struct Params {
   float* part_ml;          // [T, n_splits, H, 2]  (m in log2 units, l)
   __nv_bfloat16* out;      // [T, H, 512] when n_splits == 1
   int* status;
+  const float* sink;       // optional [H]: per-head sink logit (softmax units; one extra denominator term)
 };
 
 CB_DEVICE uint64_t desc_mn_sw128(const void* p, uint32_t lbo, uint32_t sbo) {
@@ -245,7 +246,12 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
       }
     }
     if (ok) {
-      const float inv = (p.n_splits == 1 && l > 0.f) ? 1.f / l : 1.f;
+      float lt = l;
+      if (p.sink && head_ok) {   // extra denominator term 2^(sink - m) relative to this row's running max
+        const float m_ref = m_used == -INFINITY ? 0.f : m_used;
+        lt += exp2f(p.sink[row] * 1.4426950408889634f - m_ref);
+      }
+      const float inv = (p.n_splits == 1 && lt > 0.f) ? 1.f / lt : 1.f;
 #pragma unroll 1
       for (int c = 0; c < DHALF; c += 32) {
         uint32_t v[32];
@@ -284,11 +290,13 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
 
 // out[t, h, :] = Σ_s 2^(m_s - M) O_s / Σ_s 2^(m_s - M) l_s
 __global__ void mla_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int n_splits,
-                                   int H, __nv_bfloat16* __restrict__ out) {
+                                   int H, __nv_bfloat16* __restrict__ out, const float* __restrict__ sink) {
   const int t = blockIdx.x, h = blockIdx.y;
   float M = -INFINITY;
   for (int s = 0; s < n_splits; ++s) M = fmaxf(M, part_ml[((size_t(t) * n_splits + s) * H + h) * 2]);
-  float L = 0.f;
+  const float sk = sink ? sink[h] * 1.4426950408889634f : -INFINITY;
+  M = fmaxf(M, sk);
+  float L = sink ? exp2f(sk - M) : 0.f;
   for (int s = 0; s < n_splits; ++s) {
     const float* ml = part_ml + ((size_t(t) * n_splits + s) * H + h) * 2;
     if (ml[0] != -INFINITY) L += exp2f(ml[0] - M) * ml[1];
@@ -322,7 +330,8 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // q [T,H,576], kv [S,576] bf16; idx [T,K]; out [T,H,512] bf16. part_o/part_ml: workspace for n_splits > 1
 // (sizes T*n_splits*H*512 and T*n_splits*H*2 floats).
 cudaError_t sparse_mla(const void* q, int T, int H, const void* kv, int S, const int* idx, int K, float scale,
-                       int n_splits, float* part_o, float* part_ml, void* out, int* status, cudaStream_t s) {
+                       int n_splits, float* part_o, float* part_ml, void* out, int* status, cudaStream_t s,
+                       const float* sink) {
   using namespace mla;
   if (T == 0) return cudaSuccess;
   if (H > HM || n_splits < 1) return cudaErrorInvalidValue;
@@ -362,10 +371,12 @@ cudaError_t sparse_mla(const void* q, int T, int H, const void* kv, int S, const
   p.part_o = part_o; p.part_ml = part_ml;
   p.out = reinterpret_cast<__nv_bfloat16*>(out);
   p.status = status;
+  p.sink = sink;
   sparse_mla_kernel<<<dim3(T, 2, n_splits), 256, SMEM, s>>>(tq, tkv, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || n_splits == 1) return e;
-  mla_combine_kernel<<<dim3(T, H), 128, 0, s>>>(part_o, part_ml, n_splits, H, reinterpret_cast<__nv_bfloat16*>(out));
+  mla_combine_kernel<<<dim3(T, H), 128, 0, s>>>(part_o, part_ml, n_splits, H, reinterpret_cast<__nv_bfloat16*>(out),
+                                                sink);
   return cudaGetLastError();
 }
 

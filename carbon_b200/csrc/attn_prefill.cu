@@ -46,6 +46,7 @@ struct Params {
   // optional event trace of CTA (0,0) (two-tile kernel): [0] = event count, then (clock64, kind<<32 | t<<16 | j)
   unsigned long long* trace;
   int trace_cap;
+  const float* sink;      // optional [H]: per-head sink logit (softmax units; one extra denominator term)
 };
 
 // Records one event of the traced CTA (kinds: 1 MMA saw P ready, 2 MMA issued PV+QK, 3 softmax waits for S,
@@ -311,6 +312,7 @@ __global__ void __launch_bounds__(384, 1) attn_prefill_kernel(const __grid_const
     float l_other = 0.f;
     if (ok && !exchange(n_kt, l, l_other)) { fail(kErrTimeoutTmem); ok = false; }
     l += l_other;
+    if (p.sink) l += fast_exp2(p.sink[h] * 1.4426950408889634f - (m_used == -INFINITY ? 0.f : m_used));
     if (ok) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -600,6 +602,7 @@ __global__ void __launch_bounds__(384, 1) attn_prefill2_kernel(const __grid_cons
     if (ok && nkt > 0) {
       if (!mbar_wait(&o_done[t], (nkt - 1) & 1)) { fail(kErrTimeoutTmem); ok = false; }
     }
+    if (p.sink) l += fa::fast_exp2(p.sink[h] * 1.4426950408889634f - (m_used == -INFINITY ? 0.f : m_used));
     if (ok && nkt > 0) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
@@ -634,7 +637,7 @@ __global__ void __launch_bounds__(384, 1) attn_prefill2_kernel(const __grid_cons
 // Host: q [T,H,192], kvb [T,H,256] (k_nope | v), kpe [T,64] bf16 contiguous; tiles [n_tiles] int4; out [T,H,128].
 cudaError_t attn_prefill(const void* q, const void* kvb, const void* kpe, int T, int H, const int* tiles,
                          int n_tiles, const uint32_t* mask, int mask_words, float scale, void* out, int* status,
-                         cudaStream_t s);
+                         cudaStream_t s, const float* sink);
 
 }  // namespace cb
 
@@ -668,7 +671,7 @@ static bool make_tmap_3d(CUtensorMap* m, const void* ptr, uint64_t d0, uint64_t 
 
 cudaError_t attn_prefill(const void* q, const void* kvb, const void* kpe, int T, int H, const int* tiles,
                          int n_tiles, const uint32_t* mask, int mask_words, float scale, void* out, int* status,
-                         cudaStream_t s) {
+                         cudaStream_t s, const float* sink) {
   using namespace fa;
   if (n_tiles == 0) return cudaSuccess;
   CUtensorMap tq, tkv, tkpe;
@@ -693,6 +696,7 @@ cudaError_t attn_prefill(const void* q, const void* kvb, const void* kpe, int T,
   p.status = status;
   p.trace = nullptr;
   p.trace_cap = 0;
+  p.sink = sink;
   dim3 grid(n_tiles, H);
   attn_prefill_kernel<<<grid, 384, SMEM, s>>>(tq, tkv, tkpe, p);
   return cudaGetLastError();
@@ -701,7 +705,7 @@ cudaError_t attn_prefill(const void* q, const void* kvb, const void* kpe, int T,
 // Two-tile kernel: tiles are (seq_start, seq_len, q0, 0) with q0 a multiple of 256.
 cudaError_t attn_prefill2(const void* q, const void* kvb, const void* kpe, int T, int H, const int* tiles,
                           int n_tiles, const uint32_t* mask, int mask_words, float scale, void* out, int* status,
-                          cudaStream_t s, int64_t* trace, int trace_cap) {
+                          cudaStream_t s, int64_t* trace, int trace_cap, const float* sink) {
   using namespace fa;
   if (n_tiles == 0) return cudaSuccess;
   CUtensorMap tq, tkv, tkpe;
@@ -727,6 +731,7 @@ cudaError_t attn_prefill2(const void* q, const void* kvb, const void* kpe, int T
   p.status = status;
   p.trace = reinterpret_cast<unsigned long long*>(trace);
   p.trace_cap = trace_cap;
+  p.sink = sink;
   dim3 grid(n_tiles, H);
   fa2::attn_prefill2_kernel<<<grid, 384, fa2::SMEM, s>>>(tq, tkv, tkpe, p);
   return cudaGetLastError();

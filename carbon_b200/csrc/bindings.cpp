@@ -247,7 +247,11 @@ void gemm_bf16(torch::Tensor A, torch::Tensor B, torch::Tensor out, int64_t epi,
 // q [T, H, 192], kvb [T, H, 256] (k_nope | v), kpe [T, 64] -> out [T, H, 128]
 void attn_prefill(torch::Tensor q, torch::Tensor kvb, torch::Tensor kpe, torch::Tensor tiles,
                   c10::optional<torch::Tensor> mask, double scale, torch::Tensor out,
-                  c10::optional<torch::Tensor> status, int64_t version, c10::optional<torch::Tensor> trace) {
+                  c10::optional<torch::Tensor> status, int64_t version, c10::optional<torch::Tensor> trace,
+                  c10::optional<torch::Tensor> sink) {
+  if (sink.has_value() && sink->defined()) {
+    CHECK_DT((*sink), at::kFloat); CHECK_CONTIG((*sink)); TORCH_CHECK(sink->numel() >= q.size(1));
+  }
   CHECK_CUDA(q); CHECK_DT(q, at::kBFloat16); CHECK_DT(kvb, at::kBFloat16); CHECK_DT(kpe, at::kBFloat16);
   CHECK_CONTIG(q); CHECK_CONTIG(kvb); CHECK_CONTIG(kpe); CHECK_CONTIG(out); CHECK_DT(tiles, at::kInt);
   TORCH_CHECK(q.size(2) == 192 && kvb.size(2) == 256 && kpe.size(-1) == 64, "attn_prefill: MLA dims 192/128");
@@ -267,11 +271,11 @@ void attn_prefill(torch::Tensor q, torch::Tensor kvb, torch::Tensor kpe, torch::
     }
     CK(cb::attn_prefill2(q.data_ptr(), kvb.data_ptr(), kpe.data_ptr(), T, H, tiles.data_ptr<int>(), tiles.size(0),
                          ptr_or_null<const uint32_t>(mask), words, float(scale), out.data_ptr(),
-                         ptr_or_null<int>(status), cur_stream(), tr, cap));
+                         ptr_or_null<int>(status), cur_stream(), tr, cap, ptr_or_null<const float>(sink)));
   } else {
     CK(cb::attn_prefill(q.data_ptr(), kvb.data_ptr(), kpe.data_ptr(), T, H, tiles.data_ptr<int>(), tiles.size(0),
                         ptr_or_null<const uint32_t>(mask), words, float(scale), out.data_ptr(),
-                        ptr_or_null<int>(status), cur_stream()));
+                        ptr_or_null<int>(status), cur_stream(), ptr_or_null<const float>(sink)));
   }
 }
 
@@ -296,7 +300,10 @@ void topk_mask(torch::Tensor logits, int64_t Tq, int64_t k, torch::Tensor mask, 
 
 // q [T, H, 576], kv [S, 576] bf16, idx [T, K] int32 -> out [T, H, 512] bf16
 void sparse_mla(torch::Tensor q, torch::Tensor kv, torch::Tensor idx, double scale, int64_t n_splits,
-                c10::optional<torch::Tensor> work, torch::Tensor out) {
+                c10::optional<torch::Tensor> work, torch::Tensor out, c10::optional<torch::Tensor> sink) {
+  if (sink.has_value() && sink->defined()) {
+    CHECK_DT((*sink), at::kFloat); CHECK_CONTIG((*sink)); TORCH_CHECK(sink->numel() >= q.size(1));
+  }
   CHECK_CUDA(q); CHECK_DT(q, at::kBFloat16); CHECK_DT(kv, at::kBFloat16); CHECK_DT(idx, at::kInt);
   CHECK_CONTIG(q); CHECK_CONTIG(kv); CHECK_CONTIG(idx); CHECK_CONTIG(out);
   TORCH_CHECK(q.size(2) == 576 && kv.size(1) == 576 && out.size(2) == 512);
@@ -310,7 +317,7 @@ void sparse_mla(torch::Tensor q, torch::Tensor kv, torch::Tensor idx, double sca
   }
   c10::cuda::CUDAGuard g(q.device());
   CK(cb::sparse_mla(q.data_ptr(), T, H, kv.data_ptr(), kv.size(0), idx.data_ptr<int>(), idx.size(1), float(scale),
-                    n_splits, po, pml, out.data_ptr(), nullptr, cur_stream()));
+                    n_splits, po, pml, out.data_ptr(), nullptr, cur_stream(), ptr_or_null<const float>(sink)));
 }
 
 // decode-side DSA: q [T, H, 128] bf16, w [T, H] fp32, kc [S, 128] bf16, key_slots [T, L], n_keys [T] -> out [T, k]

@@ -51,14 +51,15 @@ cudaError_t gemm_bf16(const void* A, int lda, const void* B, int ldb, int M, int
                       int num_sms, cudaStream_t s, int k_splits = 1, float* work = nullptr);
 
 // tcgen05 MLA prefill attention (attn_prefill.cu)
+// sink (optional, [H] fp32): per-head attention-sink logit
 cudaError_t attn_prefill(const void* q, const void* kvb, const void* kpe, int T, int H, const int* tiles,
                          int n_tiles, const uint32_t* mask, int mask_words, float scale, void* out, int* status,
-                         cudaStream_t s);
+                         cudaStream_t s, const float* sink = nullptr);
 
 // trace (optional, int64 [1 + 2*trace_cap], zeroed): event timeline of CTA (0,0), see attn_prefill.cu
 cudaError_t attn_prefill2(const void* q, const void* kvb, const void* kpe, int T, int H, const int* tiles,
                           int n_tiles, const uint32_t* mask, int mask_words, float scale, void* out, int* status,
-                          cudaStream_t s, int64_t* trace = nullptr, int trace_cap = 0);
+                          cudaStream_t s, int64_t* trace = nullptr, int trace_cap = 0, const float* sink = nullptr);
 
 // DSA indexer: logits GEMM with fused relu/weight/head-sum epilogue (gemm.cu) and exact top-k bitmask (topk.cu)
 cudaError_t indexer_logits(const void* keys, int L, const void* q, int Tq, int H, int Di, const float* w, float* out,
@@ -71,7 +72,9 @@ cudaError_t topk_index(const float* logits, const int* key_slots, const int* n_k
                        int* out, cudaStream_t s);
 
 // tcgen05 absorbed-MLA sparse attention over the latent cache (attn_decode.cu)
+// sink (optional, [H] fp32): per-head attention-sink logit
 cudaError_t sparse_mla(const void* q, int T, int H, const void* kv, int S, const int* idx, int K, float scale,
-                       int n_splits, float* part_o, float* part_ml, void* out, int* status, cudaStream_t s);
+                       int n_splits, float* part_o, float* part_ml, void* out, int* status, cudaStream_t s,
+                       const float* sink = nullptr);
 
 }  // namespace cb

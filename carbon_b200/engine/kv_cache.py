@@ -11,7 +11,7 @@ the native block allocator in ``carbon_b200.engine.allocator`` (C++).
 """
 from __future__ import annotations
 
-from typing import List
+from typing import List, Optional
 
 import torch
 
@@ -28,10 +28,11 @@ class PagedLatentCache:
         width = cfg.kv_lora_rank + cfg.qk_rope_head_dim
         self.latent: List[torch.Tensor] = [torch.zeros(self.num_slots, width, dtype=dtype, device=device)
                                            for _ in range(n_layers)]
-        self.index_k: List[torch.Tensor] = []
+        # indexer keys only for layers that run the indexer (index-source layers share their selection)
+        self.index_k: List[Optional[torch.Tensor]] = []
         if cfg.use_indexer:
             self.index_k = [torch.zeros(self.num_slots, cfg.index_head_dim, dtype=dtype, device=device)
-                            for _ in range(n_layers)]
+                            if cfg.has_indexer(l) else None for l in range(n_layers)]
         self.alloc = BlockAllocator(num_pages)
 
     def write_latent(self, layer: int, loc: torch.Tensor, rows: torch.Tensor) -> None:
@@ -41,9 +42,9 @@ class PagedLatentCache:
         self.index_k[layer].index_copy_(0, loc.long(), rows.to(self.index_k[layer].dtype))
 
     def bytes(self) -> int:
-        return sum(t.numel() * t.element_size() for t in self.latent + self.index_k)
+        return sum(t.numel() * t.element_size() for t in self.latent + self.index_k if t is not None)
 
     @staticmethod
     def bytes_per_token(cfg: ModelConfig, n_layers: int, elem: int = 2) -> int:
-        w = cfg.kv_lora_rank + cfg.qk_rope_head_dim + (cfg.index_head_dim if cfg.use_indexer else 0)
-        return w * elem * n_layers
+        n_idx = sum(1 for l in range(n_layers) if cfg.has_indexer(l))
+        return (cfg.kv_lora_rank + cfg.qk_rope_head_dim) * elem * n_layers + cfg.index_head_dim * elem * n_idx

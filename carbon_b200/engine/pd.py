@@ -43,8 +43,9 @@ class PrefillRole:
             slots = torch.tensor([r.pages[p // eng.page_size] * eng.page_size + p % eng.page_size for p in range(n)],
                                  dtype=torch.int64, device=eng.device)
             payload = [torch.stack([_gather_rows(c, slots) for c in eng.cache.latent])]
-            if eng.cache.index_k:
-                payload.append(torch.stack([_gather_rows(c, slots) for c in eng.cache.index_k]))
+            idx_layers = [c for c in eng.cache.index_k if c is not None]     # layers that run the indexer
+            if idx_layers:
+                payload.append(torch.stack([_gather_rows(c, slots) for c in idx_layers]))
             hdr = torch.tensor([n, t], dtype=torch.int64, device=eng.device if self.side else "cpu")
             if self.side is not None:
                 self.side.wait_stream(torch.cuda.current_stream())
@@ -90,11 +91,11 @@ class DecodeRole:
             dist.recv(lat, self.peer, group=self.group)
             for l, c in enumerate(eng.cache.latent):
                 c.index_copy_(0, slots, lat[l])
-            if eng.cache.index_k:
-                ik = torch.empty(cfg.n_layers, n, eng.cache.index_k[0].shape[1], dtype=eng.cache.index_k[0].dtype,
-                                 device=dev)
+            idx_layers = [c for c in eng.cache.index_k if c is not None]
+            if idx_layers:
+                ik = torch.empty(len(idx_layers), n, idx_layers[0].shape[1], dtype=idx_layers[0].dtype, device=dev)
                 dist.recv(ik, self.peer, group=self.group)
-                for l, c in enumerate(eng.cache.index_k):
+                for l, c in enumerate(idx_layers):
                     c.index_copy_(0, slots, ik[l])
             r.n_cached = n
             reqs.append(r)

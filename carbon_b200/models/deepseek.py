@@ -151,6 +151,7 @@ class DeepseekModel:
         self.fp8 = fp8
         self.trace = None          # set to a list to record (name, tensor) at sublayer boundaries (debugging)
         self._side = None          # side stream of the shared expert
+        self._dsa = {}
         cfg.validate()
         tp, ep = self.pctx.tp, self.pctx.ep
         self.H_local = cfg.n_heads // tp
@@ -207,7 +208,9 @@ class DeepseekModel:
         L.w_uv = wkv_b3[:, dn:, :].contiguous().to(self.act_dtype)                  # [Hl, dv, r]
         wo = get(a + "wo.weight")                                                  # [D, H*dv]
         L.wo = Lin(wo[:, h0 * dv:h1 * dv].contiguous(), dev, self.fp8)
-        if cfg.use_indexer:
+        L.sink = get(a + "sink")[h0:h1].float().contiguous() if cfg.attn_sink else None
+        L.has_indexer = cfg.has_indexer(i)
+        if L.has_indexer:
             ix = a + "indexer."
             L.idx_wq = Lin(get(ix + "wq.weight"), dev, fp8=False)
             L.idx_wk = Lin(get(ix + "wk.weight"), dev, fp8=False)
@@ -312,7 +315,7 @@ class DeepseekModel:
             C.rope_(k_pe, 0, dr, self.cos_sin, pos_l)
             latent_l = torch.cat([kv_c.to(self.act_dtype), k_pe.view(-1, dr).to(self.act_dtype)], dim=-1)
         idx_l = None
-        if cfg.use_indexer:
+        if L.has_indexer:
             with region("attn.indexer_qk"):
                 idx_l = self.indexer_qkw(i, h, q_lat_l, pos_l)
         q_lat_a = q_lat_l.to(self.act_dtype) if self.on_gpu else q_lat_l
@@ -385,10 +388,16 @@ class DeepseekModel:
                 cu = [0, 0]
         with region("attn.kv_up"):
             kvb = L.wkv_b(latent[:, :r].contiguous()).view(T, Hl, dn + dv)
-        with region("attn.indexer_topk"):
-            masks = self._prefill_key_masks(idx_l, fb, gather=not dp) if idx_l is not None else None
+        src = cfg.index_source(i)
+        masks = None
+        if src == i:
+            with region("attn.indexer_topk"):
+                masks = self._prefill_key_masks(idx_l, fb, gather=not dp)
+            self._dsa[i] = masks
+        elif src is not None:
+            masks = self._dsa.get(src)              # selection shared with the index-source layer
         with region("attn.core_prefill"):
-            return A.mla_prefill(q, kvb, latent[:, r:].contiguous(), cu, cfg.softmax_scale, masks)
+            return A.mla_prefill(q, kvb, latent[:, r:].contiguous(), cu, cfg.softmax_scale, masks, sink=L.sink)
 
     def _attn_decode(self, i, q, fb, cache, idx_l, dp: bool = False):
         cfg, L, pc = self.cfg, self.layers[i], self.pctx
@@ -399,14 +408,19 @@ class DeepseekModel:
             q_abs = head_bmm(q[..., :dn], L.w_uk)                                    # [T, Hl, r]
             qf = torch.cat([q_abs.to(self.act_dtype), q[..., dn:].to(self.act_dtype)], dim=-1).contiguous()
         idx = fb.key_slots[lo:hi] if dp else fb.key_slots
-        if idx_l is not None and int(fb.key_slots.shape[1]) > cfg.index_topk:
-            with region("attn.indexer_topk"):
-                qi, _, wi = idx_l
-                sel = A.indexer_topk(qi, wi, cache.index_k[i], fb.key_slots[lo:hi].contiguous(),
-                                     fb.n_keys[lo:hi].contiguous(), cfg.index_topk)
-                idx = sel if dp else pc.gather_rows(sel)
+        src = cfg.index_source(i)
+        if src is not None and int(fb.key_slots.shape[1]) > cfg.index_topk:
+            if src == i:
+                with region("attn.indexer_topk"):
+                    qi, _, wi = idx_l
+                    sel = A.indexer_topk(qi, wi, cache.index_k[i], fb.key_slots[lo:hi].contiguous(),
+                                         fb.n_keys[lo:hi].contiguous(), cfg.index_topk)
+                    idx = sel if dp else pc.gather_rows(sel)
+                self._dsa[i] = idx
+            else:
+                idx = self._dsa[src]                # selection shared with the index-source layer
         with region("attn.core_decode"):
-            o_lat = A.sparse_mla(qf, cache.latent[i], idx.contiguous(), cfg.softmax_scale, r)   # [T, Hl, r]
+            o_lat = A.sparse_mla(qf, cache.latent[i], idx.contiguous(), cfg.softmax_scale, r, sink=L.sink)
         with region("attn.absorb_o"):
             return head_bmm(o_lat, L.w_uv)                                           # [T, Hl, dv]
 
@@ -488,6 +502,7 @@ class DeepseekModel:
         cfg = self.cfg
         T_all = fb.ids.shape[0]
         self.pctx.set_bounds(fb.bounds if fb.bounds is not None else [0, T_all])
+        self._dsa = {}                 # DSA selections of this forward's index-source layers
         with region("embed"):
             X, sumsq = self.embed_tokens(fb.ids)
         for i in range(cfg.n_layers):

@@ -24,14 +24,15 @@ from ._ext import ext
 
 
 def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens: List[int], scale: float,
-                      key_masks=None, version: int = 2, trace: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Reference-layout entry: q [T,H,dqk], k [T,H,dqk], v [T,H,dv]."""
+                      key_masks=None, version: int = 2, trace: Optional[torch.Tensor] = None,
+                      sink: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Reference-layout entry: q [T,H,dqk], k [T,H,dqk], v [T,H,dv]; sink [H]: per-head attention-sink logit."""
     T, H, dv = q.shape[0], q.shape[1], v.shape[2]
     if q.is_cuda and q.shape[2] == 192 and dv == 128:
         dn = 128
         kvb = torch.cat([k[..., :dn], v], dim=-1).contiguous()
         kpe = k[:, 0, dn:].contiguous()
-        return mla_prefill(q, kvb, kpe, cu_seqlens, scale, key_masks, version, trace)
+        return mla_prefill(q, kvb, kpe, cu_seqlens, scale, key_masks, version, trace, sink)
     out = torch.empty(T, H, dv, dtype=torch.float32, device=q.device)
     if isinstance(key_masks, torch.Tensor):
         key_masks = unpack_key_mask(key_masks, cu_seqlens)
@@ -39,12 +40,13 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seql
         s, t = cu_seqlens[b], cu_seqlens[b + 1]
         pos = torch.arange(t - s, device=q.device)
         m = key_masks[b] if key_masks is not None else None
-        out[s:t] = R.causal_attention(q[s:t], k[s:t], v[s:t], scale, pos, pos, m)
+        out[s:t] = R.causal_attention(q[s:t], k[s:t], v[s:t], scale, pos, pos, m, sink=sink)
     return out
 
 
 def mla_prefill(q: torch.Tensor, kvb: torch.Tensor, kpe: torch.Tensor, cu_seqlens: List[int], scale: float,
-                key_masks=None, version: int = 2, trace: Optional[torch.Tensor] = None) -> torch.Tensor:
+                key_masks=None, version: int = 2, trace: Optional[torch.Tensor] = None,
+                sink: Optional[torch.Tensor] = None) -> torch.Tensor:
     """MLA prefill in the projection's own layout: q [T,H,192], kvb [T,H,256] = (k_nope | v) straight from the
     wkv_b GEMM, kpe [T,64] the shared RoPE key (k = [k_nope, kpe] per head). Returns o [T,H,128].
     version 2: two 128-row Q tiles per CTA sharing each K/V tile (the default); 1: one Q tile per CTA."""
@@ -52,7 +54,7 @@ def mla_prefill(q: torch.Tensor, kvb: torch.Tensor, kpe: torch.Tensor, cu_seqlen
     if not q.is_cuda:
         dn = q.shape[2] - kpe.shape[-1]
         k = torch.cat([kvb[..., :dn], kpe.view(T, 1, -1).expand(T, H, kpe.shape[-1])], dim=-1)
-        return prefill_attention(q, k, kvb[..., dn:], cu_seqlens, scale, key_masks)
+        return prefill_attention(q, k, kvb[..., dn:], cu_seqlens, scale, key_masks, sink=sink)
     mask = None
     if isinstance(key_masks, torch.Tensor):
         mask = key_masks
@@ -61,7 +63,7 @@ def mla_prefill(q: torch.Tensor, kvb: torch.Tensor, kpe: torch.Tensor, cu_seqlen
     out = torch.empty(T, H, 128, dtype=torch.bfloat16, device=q.device)
     tiles = prefill_tiles(cu_seqlens, 256 if version == 2 else 128).to(q.device, non_blocking=True)
     ext().attn_prefill(q.contiguous(), kvb.contiguous(), kpe.contiguous(), tiles, mask, float(scale), out, None,
-                       version, trace)
+                       version, trace, sink.float().contiguous() if sink is not None else None)
     return out
 
 
@@ -138,8 +140,10 @@ def mla_splits(T: int, K: int, device) -> int:
     return max(1, min(s, (K + 127) // 128))
 
 
-def sparse_mla(q: torch.Tensor, kv: torch.Tensor, idx: torch.Tensor, scale: float, d_latent: int) -> torch.Tensor:
-    """Absorbed MQA over latent rows: q [T,H,D], kv [S,D], idx [T,K] int32 (-1 pad) -> o_lat [T,H,d_latent]."""
+def sparse_mla(q: torch.Tensor, kv: torch.Tensor, idx: torch.Tensor, scale: float, d_latent: int,
+               sink: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Absorbed MQA over latent rows: q [T,H,D], kv [S,D], idx [T,K] int32 (-1 pad) -> o_lat [T,H,d_latent].
+    sink [H]: per-head attention-sink logit (an extra softmax denominator term)."""
     T, H, D = q.shape
     if q.is_cuda:
         e = ext()
@@ -147,14 +151,10 @@ def sparse_mla(q: torch.Tensor, kv: torch.Tensor, idx: torch.Tensor, scale: floa
             out = torch.empty(T, H, d_latent, dtype=torch.bfloat16, device=q.device)
             splits = mla_splits(T, idx.shape[1], q.device)
             work = torch.empty(T * splits * H * 514, dtype=torch.float32, device=q.device) if splits > 1 else None
-            e.sparse_mla(q, kv, idx, float(scale), splits, work, out)
+            e.sparse_mla(q, kv, idx, float(scale), splits, work, out,
+                         sink.float().contiguous() if sink is not None else None)
             return out
-        # temporary path until the tcgen05 sparse-MLA kernel is registered
-        sel = kv[idx.clamp(min=0).long()].float()                      # [T, K, D]
-        s = torch.einsum("thd,tkd->thk", q.float(), sel) * scale
-        s = s.masked_fill((idx < 0)[:, None, :], float("-inf"))
-        p = torch.softmax(s, dim=-1)
-        return torch.einsum("thk,tkd->thd", p, sel[..., :d_latent]).to(torch.bfloat16)
+        raise RuntimeError("sparse_mla: the tcgen05 kernel needs D=576 (512 latent + 64 RoPE), d_latent=512, H<=128")
     out = torch.zeros(T, H, d_latent)
     for t in range(T):
         sel = idx[t][idx[t] >= 0].long()
@@ -162,7 +162,11 @@ def sparse_mla(q: torch.Tensor, kv: torch.Tensor, idx: torch.Tensor, scale: floa
             continue
         keys = kv[sel].float()
         s = (q[t].float() @ keys.t()) * scale
-        p = torch.softmax(s, dim=-1)
+        if sink is not None:
+            s = torch.cat([s, sink.float()[:, None]], dim=-1)
+            p = torch.softmax(s, dim=-1)[:, :-1]
+        else:
+            p = torch.softmax(s, dim=-1)
         out[t] = p @ keys[:, :d_latent]
     return out
 

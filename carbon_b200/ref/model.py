@@ -49,7 +49,9 @@ def param_shapes(cfg: ModelConfig) -> "OrderedDict[str, Tuple[Tuple[int, ...], s
         p[L + "attn.kv_norm.weight"] = ((cfg.kv_lora_rank,), "ones")
         p[L + "attn.wkv_b.weight"] = ((H * (cfg.qk_nope_head_dim + cfg.v_head_dim), cfg.kv_lora_rank), "normal")
         p[L + "attn.wo.weight"] = ((D, H * cfg.v_head_dim), "normal")
-        if cfg.use_indexer:
+        if cfg.attn_sink:
+            p[L + "attn.sink"] = ((H,), "normal")
+        if cfg.has_indexer(i):
             qin = cfg.q_lora_rank if cfg.q_lora_rank > 0 else D
             p[L + "attn.indexer.wq.weight"] = ((cfg.index_n_heads * cfg.index_head_dim, qin), "normal")
             p[L + "attn.indexer.wk.weight"] = ((cfg.index_head_dim, D), "normal")
@@ -108,6 +110,7 @@ class RefModel:
         self.cfg = cfg
         self.w = {k: v.float() for k, v in weights.items()}
         self.forced_routing = None   # {layer: ids [T, k]}: use these expert choices instead of the router's top-k
+        self._dsa = {}               # DSA selection of each index-source layer in the current forward
 
     # -- sublayers -------------------------------------------------------------------------------------------------
     def attention(self, i: int, h: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
@@ -130,9 +133,14 @@ class RefModel:
         v = kvb[..., dn:]
         qf = torch.cat([q_nope, q_pe], dim=-1)
         allowed = None
-        if cfg.use_indexer:
+        src = cfg.index_source(i)
+        if src == i:
             allowed = ops.topk_mask(self.indexer_logits(i, h, q_lat, pos), pos, pos, cfg.index_topk)
-        o = ops.causal_attention(qf, k, v, cfg.softmax_scale, pos, pos, allowed)
+            self._dsa[i] = allowed
+        elif src is not None:
+            allowed = self._dsa[src]           # shared selection of the source layer
+        sink = w[L + "sink"] if cfg.attn_sink else None
+        o = ops.causal_attention(qf, k, v, cfg.softmax_scale, pos, pos, allowed, sink=sink)
         return o.reshape(T, H * dv) @ w[L + "wo.weight"].t()
 
     def indexer_logits(self, i: int, h: torch.Tensor, q_lat: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
@@ -192,6 +200,7 @@ class RefModel:
         cfg, w = self.cfg, self.w
         T = ids.shape[0]
         pos = torch.arange(T) if pos is None else pos
+        self._dsa = {}
         X = w["embed.weight"][ids.long()][:, None, :].expand(T, cfg.hc_mult, cfg.hidden_size).clone()
         for i in range(cfg.n_layers):
             L = f"layers.{i}."

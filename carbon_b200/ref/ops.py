@@ -211,9 +211,10 @@ def _stable_topk(key: torch.Tensor, k: int) -> torch.Tensor:
 # attention
 # ----------------------------------------------------------------------------------------------------------------------
 def causal_attention(q, k, v, scale: float, q_pos: torch.Tensor, k_pos: torch.Tensor,
-                     allowed: Optional[torch.Tensor] = None) -> torch.Tensor:
+                     allowed: Optional[torch.Tensor] = None, sink: Optional[torch.Tensor] = None) -> torch.Tensor:
     """q [Tq,H,dq], k [Tk,H,dq] or [Tk,1,dq], v [Tk,H,dv] or [Tk,1,dv].
-    Mask: k_pos <= q_pos, and (if given) allowed[Tq, Tk] bool. Returns [Tq, H, dv] fp32."""
+    Mask: k_pos <= q_pos, and (if given) allowed[Tq, Tk] bool.  sink [H]: one extra logit per head in the softmax
+    denominator (it takes probability mass but has no value row).  Returns [Tq, H, dv] fp32."""
     qf, kf, vf = q.float(), k.float(), v.float()
     if kf.shape[1] == 1:
         kf = kf.expand(-1, qf.shape[1], -1)
@@ -224,7 +225,11 @@ def causal_attention(q, k, v, scale: float, q_pos: torch.Tensor, k_pos: torch.Te
     if allowed is not None:
         mask = mask & allowed
     s = s.masked_fill(~mask[None], float("-inf"))
-    p = torch.softmax(s, dim=-1)
+    if sink is not None:
+        s = torch.cat([s, sink.float()[:, None, None].expand(-1, s.shape[1], 1)], dim=-1)
+        p = torch.softmax(s, dim=-1)[..., :-1]
+    else:
+        p = torch.softmax(s, dim=-1)
     return torch.einsum("hqk,khd->qhd", p, vf)
 
 

@@ -8,8 +8,16 @@ from carbon_b200.models.weights import WeightSource
 from carbon_b200.ref.model import RefModel, init_weights
 
 
-def test_tiny_engine_matches_oracle():
+import pytest
+
+
+@pytest.mark.parametrize("variant", ["v3", "v41_features"])
+def test_tiny_engine_matches_oracle(variant):
+    """v41_features: DSA selection computed by index-source layers 1 and 3 only (layer 0 dense, layer 2 reuses
+    layer 1's selection) and per-head attention sinks."""
     cfg = tiny_config()
+    if variant == "v41_features":
+        cfg = cfg.replace(n_layers=4, index_sources=(1, 3), attn_sink=True)
     w = init_weights(cfg, seed=0)
     ref = RefModel(cfg, w)
     g = torch.Generator().manual_seed(1)

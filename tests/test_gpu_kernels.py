@@ -285,10 +285,21 @@ def test_mhc_kernels():
                                                 ([200, 260], True, 1.0), ([1000, 700], False, 4.0),
                                                 ([1300], True, 3.0), ([256, 384, 129], False, 1.0)])
 def test_attn_prefill(lens, masked, qscale, version):
+    _check_attn_prefill(lens, masked, qscale, version, with_sink=False)
+
+
+@pytest.mark.parametrize("version", [1, 2])
+@pytest.mark.parametrize("lens,masked", [([300, 77], False), ([513], True)])
+def test_attn_prefill_with_sink(lens, masked, version):
+    _check_attn_prefill(lens, masked, 1.0, version, with_sink=True)
+
+
+def _check_attn_prefill(lens, masked, qscale, version, with_sink):
     from carbon_b200.ops.attention import prefill_attention
 
     torch.manual_seed(5)
     H = 4
+    sink = torch.randn(H) * 2 if with_sink else None
     T = sum(lens)
     q = (torch.randn(T, H, 192) * qscale).to(torch.bfloat16)     # qscale > 1: row maxima keep growing (rescales)
     k = torch.randn(T, H, 192).to(torch.bfloat16)
@@ -303,12 +314,14 @@ def test_attn_prefill(lens, masked, qscale, version):
         for m in masks:
             m.fill_diagonal_(True)
     out = prefill_attention(q.to(DEV), k.to(DEV), v.to(DEV), cu, 192 ** -0.5,
-                            [m.to(DEV) for m in masks] if masks else None, version=version)
+                            [m.to(DEV) for m in masks] if masks else None, version=version,
+                            sink=sink.to(DEV) if with_sink else None)
     torch.cuda.synchronize()
     for b in range(len(lens)):
         s, t = cu[b], cu[b + 1]
         pos = torch.arange(t - s)
-        ref = R.causal_attention(q[s:t], k[s:t], v[s:t], 192 ** -0.5, pos, pos, masks[b] if masks else None)
+        ref = R.causal_attention(q[s:t], k[s:t], v[s:t], 192 ** -0.5, pos, pos, masks[b] if masks else None,
+                                 sink=sink)
         assert rel_err(out[s:t], ref) < 1e-2, (b, rel_err(out[s:t], ref))
 
 
@@ -345,10 +358,13 @@ def test_topk_mask_exact(n, k):
 
 @pytest.mark.parametrize("T,H,K,S,splits_override", [(3, 128, 300, 1000, None), (16, 16, 64, 200, None),
                                                       (2, 128, 2048, 5000, None), (40, 64, 100, 300, None)])
-def test_sparse_mla_decode(T, H, K, S, splits_override):
+@pytest.mark.parametrize("with_sink", [False, True])
+def test_sparse_mla_decode(T, H, K, S, splits_override, with_sink):
+    """with_sink: per-head attention-sink logits (single-split normalisation and the split combine)."""
     from carbon_b200.ops.attention import sparse_mla
 
     torch.manual_seed(8)
+    sink = torch.randn(H) * 2 if with_sink else None
     q = (torch.randn(T, H, 576) * 0.5).to(torch.bfloat16)
     kv = torch.randn(S, 576).to(torch.bfloat16)
     idx = torch.randint(0, S, (T, K), dtype=torch.int32)
@@ -356,9 +372,9 @@ def test_sparse_mla_decode(T, H, K, S, splits_override):
     if T > 1:
         idx[1, 5:] = -1                    # a short row
     scale = 192 ** -0.5
-    out = sparse_mla(q.to(DEV), kv.to(DEV), idx.to(DEV), scale, 512)
+    out = sparse_mla(q.to(DEV), kv.to(DEV), idx.to(DEV), scale, 512, sink=sink.to(DEV) if with_sink else None)
     torch.cuda.synchronize()
-    ref = sparse_mla(q.float(), kv.float(), idx, scale, 512)
+    ref = sparse_mla(q.float(), kv.float(), idx, scale, 512, sink=sink)
     assert rel_err(out, ref) < 1e-2, rel_err(out, ref)
 
 
