@@ -239,7 +239,8 @@ def main(argv=None):
     ap.add_argument("--k", type=int, default=7168)
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--hidden", type=int, default=7168)
-    ap.add_argument("--attn-version", type=int, default=2, help="attn: 2 = two Q tiles per CTA, 1 = one")
+    ap.add_argument("--attn-version", type=int, default=2,
+                    help="attn: 3 = two Q tiles, 64-key steps, double-buffered S; 2 = two Q tiles, 128-key steps; 1 = one")
     ap.add_argument("--pair", type=int, default=-1, help="gemm: -1 auto, 1 CTA-pair 256x256 tiles, 0 128x128 tiles")
     a = ap.parse_args(argv)
     sys.path.insert(0, ROOT)

@@ -633,6 +633,279 @@ __global__ void __launch_bounds__(384, 1) attn_prefill2_kernel(const __grid_cons
 
 }  // namespace fa2
 
+// ---------------------------------------------------------------------------------------------------------------
+// Two-tile kernel with 64-key steps and double-buffered S (the default): per step a KV tile of 64 keys is 40 KB,
+// so the 16-slot ring (8 KB chunks) holds three steps of K/V and loads run well ahead; each Q tile has two 64-column
+// S buffers in TMEM, so QK(j+2) is issued right after PV(j) and the softmax of a tile runs back to back.
+//   MMA order: QK0(0) QK1(0) QK0(1) QK1(1) | PV0(0) QK0(2) PV1(0) QK1(2) | PV0(1) QK0(3) ...
+// TMEM of tile t: S buffers at 256t + {0, 64} (P, bf16, over the first 32 columns of the buffer), O at 256t + 128.
+// ---------------------------------------------------------------------------------------------------------------
+namespace fa3 {
+
+constexpr int BM = 128, BN = 64, DQK = 192, DV = 128;
+constexpr int QATOM = 128 * 128;                // Q: 128 rows x 64 dims
+constexpr int Q_BYTES = 3 * QATOM;
+constexpr int CH = 64 * 128;                    // ring chunk: 64 keys x 64 dims (one 128-byte-swizzled box)
+constexpr int NCH = 16;
+constexpr int CH_PER_KV = 5;                    // K: k_nope 0-63, 64-127, RoPE key; V: dv 0-63, 64-127
+constexpr int SMEM = 1024 + 2 * Q_BYTES + NCH * CH + 512;
+constexpr float kRescaleThresh = 8.0f;
+
+__global__ void __launch_bounds__(384, 1) attn_prefill3_kernel(const __grid_constant__ CUtensorMap tm_q,
+                                                               const __grid_constant__ CUtensorMap tm_kv,
+                                                               const __grid_constant__ CUtensorMap tm_kpe,
+                                                               const fa::Params p) {
+#if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 1000
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sR = sQ + 2 * Q_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sR + NCH * CH);
+  uint64_t* q_full = bars;                     // 1
+  uint64_t* r_full = bars + 1;                 // [NCH]
+  uint64_t* r_empty = bars + 1 + NCH;          // [NCH]
+  uint64_t* s_full = bars + 1 + 2 * NCH;       // [2 tiles][2 buffers]
+  uint64_t* p_full = bars + 5 + 2 * NCH;       // [2]
+  uint64_t* o_done = bars + 7 + 2 * NCH;       // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9 + 2 * NCH);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int4 tile = p.tiles[blockIdx.x];
+  const int seq_start = tile.x, seq_len = tile.y, q0 = tile.z;
+  const int h = blockIdx.y;
+  int n_kt_t[2];
+  for (int t = 0; t < 2; ++t) {
+    const int qt0 = q0 + BM * t;
+    n_kt_t[t] = qt0 < seq_len ? (min(qt0 + BM, seq_len) + BN - 1) / BN : 0;
+  }
+  const int n_kt = max(n_kt_t[0], n_kt_t[1]);
+  const bool two = n_kt_t[1] > 0;
+
+  const uint32_t warp = warp_id(), lane = lane_id();
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < NCH; ++i) { mbar_init(&r_full[i], 1); mbar_init(&r_empty[i], 1); }
+    for (int i = 0; i < 4; ++i) mbar_init(&s_full[i], 1);
+    for (int t = 0; t < 2; ++t) { mbar_init(&p_full[t], 128); mbar_init(&o_done[t], 1); }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 2) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  auto fail = [&](int code) { if (p.status) atomicCAS(p.status, 0, code); *abort_flag = 1; };
+  auto chunk = [&](int idx) -> uint8_t* { return sR + (idx % NCH) * CH; };
+
+  if (warp == 0) {
+    // ================= TMA producer: Q once, then K(j), V(j) chunks in step order =================
+    if (elect_one()) {
+      tma_prefetch_desc(&tm_q); tma_prefetch_desc(&tm_kv); tma_prefetch_desc(&tm_kpe);
+      mbar_arrive_expect_tx(q_full, (two ? 2 : 1) * Q_BYTES);
+      for (int t = 0; t < (two ? 2 : 1); ++t)
+        for (int a = 0; a < 3; ++a)
+          tma_load_3d(sQ + t * Q_BYTES + a * QATOM, &tm_q, q_full, a * 64, h, seq_start + q0 + BM * t);
+      for (int idx = 0; idx < n_kt * CH_PER_KV && !*abort_flag; ++idx) {
+        const int slot = idx % NCH, use = idx / NCH;
+        if (!mbar_wait(&r_empty[slot], (use & 1) ^ 1)) { fail(kErrTimeoutEmpty); break; }
+        mbar_arrive_expect_tx(&r_full[slot], CH);
+        const int j = idx / CH_PER_KV, c = idx % CH_PER_KV;
+        const int row = seq_start + j * BN;
+        if (c < 2) tma_load_3d(sR + slot * CH, &tm_kv, &r_full[slot], c * 64, h, row);
+        else if (c == 2) tma_load_2d(sR + slot * CH, &tm_kpe, &r_full[slot], 0, row);
+        else tma_load_3d(sR + slot * CH, &tm_kv, &r_full[slot], 128 + (c - 3) * 64, h, row);
+      }
+    }
+  } else if (warp == 1) {
+    // ================= MMA issuer =================
+    if (elect_one()) {
+      const uint32_t id_qk = idesc_bf16(BM, BN);
+      const uint32_t id_pv = fa::idesc_bf16_bmn(BM, 64);
+      bool ok = mbar_wait(q_full, 0);
+      if (!ok) fail(kErrTimeoutFull);
+      auto wait_chunks = [&](int first, int n) -> bool {
+        for (int i = 0; i < n; ++i) {
+          const int idx = first + i;
+          if (!mbar_wait(&r_full[idx % NCH], (idx / NCH) & 1)) { fail(kErrTimeoutFull); return false; }
+        }
+        tc_fence_after();
+        return true;
+      };
+      auto release_chunks = [&](int first, int n) {
+        for (int i = 0; i < n; ++i) mma_commit(&r_empty[(first + i) % NCH]);
+      };
+      auto qk = [&](int t, int j) {
+        const int kc = j * CH_PER_KV;
+        const uint32_t d = tmem + 256 * t + 64 * (j & 1);
+#pragma unroll
+        for (int k = 0; k < DQK / 16; ++k) {
+          const int a = k >> 2, off = (k & 3) * 32;
+          mma_f16_ss(d, smem_desc_sw128(sQ + t * Q_BYTES + a * QATOM + off), smem_desc_sw128(chunk(kc + a) + off),
+                     id_qk, k > 0);
+        }
+        mma_commit(&s_full[2 * t + (j & 1)]);
+      };
+      auto pv = [&](int t, int j) {
+        const int vc = j * CH_PER_KV + 3;
+        const uint32_t pcol = tmem + 256 * t + 64 * (j & 1);
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint8_t* v = chunk(vc + half);
+#pragma unroll
+          for (int k = 0; k < BN / 16; ++k)
+            mma_f16_ts(tmem + 256 * t + 128 + 64 * half, pcol + 8 * k,
+                       fa::desc_mn_sw128(v + k * 16 * 128, CH, 1024), id_pv, (j > 0 || k > 0) ? 1u : 0u);
+        }
+        mma_commit(&o_done[t]);
+      };
+      // prologue: the S of the first two steps of both tiles
+      for (int j = 0; ok && j < 2 && j < n_kt; ++j) {
+        ok = wait_chunks(j * CH_PER_KV, 3);
+        if (!ok) break;
+        for (int t = 0; t < 2; ++t)
+          if (j < n_kt_t[t]) qk(t, j);
+        release_chunks(j * CH_PER_KV, 3);
+      }
+      for (int j = 0; ok && j < n_kt && !*abort_flag; ++j) {
+        bool v_ready = false, k_ready = false;
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (j >= n_kt_t[t]) continue;
+          if (!mbar_wait(&p_full[t], j & 1)) { fail(kErrTimeoutTmem); ok = false; break; }
+          fa::trace_event(p, 1, t, j);
+          tc_fence_after();
+          if (!v_ready) { ok = wait_chunks(j * CH_PER_KV + 3, 2); v_ready = true; if (!ok) break; }
+          pv(t, j);
+          if (j + 2 < n_kt_t[t]) {
+            if (!k_ready) { ok = wait_chunks((j + 2) * CH_PER_KV, 3); k_ready = true; if (!ok) break; }
+            qk(t, j + 2);
+          }
+          fa::trace_event(p, 2, t, j);
+        }
+        if (!ok) break;
+        release_chunks(j * CH_PER_KV + 3, 2);
+        if (j + 2 < n_kt) release_chunks((j + 2) * CH_PER_KV, 3);
+      }
+    }
+  } else if (warp >= 4) {
+    // ================= softmax: tile t = (warp-4)/4, TMEM lane quadrant q, one query row per thread =================
+    const int t = int(warp - 4) >> 2;
+    const uint32_t q = warp & 3;
+    const int row = int(q * 32 + lane);
+    const int qt0 = q0 + BM * t;
+    const int qi = qt0 + row;
+    const int tok = seq_start + qi;
+    const uint32_t t_lane = tmem + ((q * 32) << 16) + 256 * t;
+    const int nkt = n_kt_t[t];
+    float m_used = -INFINITY, l = 0.f;
+    bool ok = true;
+    const bool tracer = (q == 0 && lane == 0);
+    for (int j = 0; j < nkt; ++j) {
+      const int b = j & 1;
+      if (tracer) fa::trace_event(p, 3, t, j);
+      if (!mbar_wait(&s_full[2 * t + b], (j >> 1) & 1)) { fail(kErrTimeoutTmem); ok = false; break; }
+      if (tracer) fa::trace_event(p, 4, t, j);
+      tc_fence_after();
+      float sv[64];
+      {
+        uint32_t (&r0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[0]);
+        uint32_t (&r1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[32]);
+        tmem_ld_32x32b_x32(t_lane + 64 * b, r0);
+        tmem_ld_32x32b_x32(t_lane + 64 * b + 32, r1);
+        tmem_ld_wait();
+      }
+      const int k0 = j * BN;
+      uint32_t mw0 = 0xffffffffu, mw1 = 0xffffffffu;
+      if (p.mask && qi < seq_len) {
+        const int wi = k0 >> 5;
+        mw0 = wi < p.mask_words ? p.mask[size_t(tok) * p.mask_words + wi] : 0u;
+        mw1 = wi + 1 < p.mask_words ? p.mask[size_t(tok) * p.mask_words + wi + 1] : 0u;
+      }
+      const bool full_row = (k0 + BN - 1 <= qi) && ((mw0 & mw1) == 0xffffffffu);
+      float pm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (__all_sync(0xffffffffu, full_row)) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) pm[i & 3] = fmaxf(pm[i & 3], sv[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const bool allowed = (k0 + i <= qi) && ((((i < 32) ? mw0 : mw1) >> (i & 31)) & 1u);
+          sv[i] = allowed ? sv[i] : -INFINITY;
+          pm[i & 3] = fmaxf(pm[i & 3], sv[i]);
+        }
+      }
+      float mt = fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3]));
+      mt = mt == -INFINITY ? mt : mt * p.scale_log2;
+      const bool need = (j > 0) && (mt > m_used + kRescaleThresh);
+      const float m_new = (need || j == 0) ? fmaxf(m_used, mt) : m_used;
+      const float m_ref = m_new == -INFINITY ? 0.f : m_new;
+      float alpha = 1.f;
+      if (need && m_used != -INFINITY) alpha = fa::fast_exp2(m_used - m_ref);
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // O holds the sums of earlier steps at the old max: wait for the last PV, then rescale it in TMEM
+        if (!mbar_wait(&o_done[t], (j - 1) & 1)) { fail(kErrTimeoutTmem); ok = false; break; }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < DV; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(t_lane + 128 + c, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
+          tmem_st_32x32b_x32(t_lane + 128 + c, r);
+        }
+      }
+      float rsp[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t pk[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const float a = fa::fast_exp2(fmaf(sv[2 * i], p.scale_log2, -m_ref));
+        const float c = fa::fast_exp2(fmaf(sv[2 * i + 1], p.scale_log2, -m_ref));
+        rsp[i & 3] += a + c;
+        pk[i] = pack_bf16x2(a, c);
+      }
+      tmem_st_32x32b_x32(t_lane + 64 * b, pk);     // P over the first 32 columns of this S buffer
+      l = l * alpha + ((rsp[0] + rsp[1]) + (rsp[2] + rsp[3]));
+      m_used = m_new;
+      tmem_st_wait();
+      tc_fence_before();
+      if (tracer) fa::trace_event(p, 5, t, j);
+      mbar_arrive(&p_full[t]);
+    }
+    if (p.sink) l += fa::fast_exp2(p.sink[h] * 1.4426950408889634f - (m_used == -INFINITY ? 0.f : m_used));
+    if (ok && nkt > 0) {
+      if (!mbar_wait(&o_done[t], (nkt - 1) & 1)) { fail(kErrTimeoutTmem); ok = false; }
+    }
+    if (ok && nkt > 0) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      __nv_bfloat16* o = p.out + (size_t(tok) * p.H + h) * DV;
+#pragma unroll 1
+      for (int c = 0; c < DV; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_lane + 128 + c, r);
+        tmem_ld_wait();
+        if (qi < seq_len) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            uint4 w;
+            w.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]) * inv, __uint_as_float(r[8 * v + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]) * inv, __uint_as_float(r[8 * v + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * inv, __uint_as_float(r[8 * v + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * inv, __uint_as_float(r[8 * v + 7]) * inv);
+            reinterpret_cast<uint4*>(o + c)[v] = w;
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 2) { tc_fence_after(); tmem_dealloc(tmem, 512); }
+#endif
+}
+
+}  // namespace fa3
+
 
 // Host: q [T,H,192], kvb [T,H,256] (k_nope | v), kpe [T,64] bf16 contiguous; tiles [n_tiles] int4; out [T,H,128].
 cudaError_t attn_prefill(const void* q, const void* kvb, const void* kpe, int T, int H, const int* tiles,
@@ -734,6 +1007,41 @@ cudaError_t attn_prefill2(const void* q, const void* kvb, const void* kpe, int T
   p.sink = sink;
   dim3 grid(n_tiles, H);
   fa2::attn_prefill2_kernel<<<grid, 384, fa2::SMEM, s>>>(tq, tkv, tkpe, p);
+  return cudaGetLastError();
+}
+
+// 64-key-step kernel (fa3): tiles as for attn_prefill2.
+cudaError_t attn_prefill3(const void* q, const void* kvb, const void* kpe, int T, int H, const int* tiles,
+                          int n_tiles, const uint32_t* mask, int mask_words, float scale, void* out, int* status,
+                          cudaStream_t s, int64_t* trace, int trace_cap, const float* sink) {
+  using namespace fa;
+  if (n_tiles == 0) return cudaSuccess;
+  CUtensorMap tq, tkv, tkpe;
+  if (!make_tmap_3d(&tq, q, DQK, H, T, DQK * 2, uint64_t(H) * DQK * 2, 64, 1, 128) ||
+      !make_tmap_3d(&tkv, kvb, 256, H, T, 256 * 2, uint64_t(H) * 256 * 2, 64, 1, fa3::BN) ||
+      !make_tmap_2d(&tkpe, kpe, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64, T, 64 * 2, 64, fa3::BN,
+                    CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  static bool attr = false;
+  if (!attr) {
+    cudaError_t e = cudaFuncSetAttribute(fa3::attn_prefill3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         fa3::SMEM);
+    if (e != cudaSuccess) return e;
+    attr = true;
+  }
+  Params p;
+  p.tiles = reinterpret_cast<const int4*>(tiles);
+  p.mask = mask;
+  p.mask_words = mask_words;
+  p.H = H;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.status = status;
+  p.trace = reinterpret_cast<unsigned long long*>(trace);
+  p.trace_cap = trace_cap;
+  p.sink = sink;
+  dim3 grid(n_tiles, H);
+  fa3::attn_prefill3_kernel<<<grid, 384, fa3::SMEM, s>>>(tq, tkv, tkpe, p);
   return cudaGetLastError();
 }
 

@@ -261,7 +261,7 @@ void attn_prefill(torch::Tensor q, torch::Tensor kvb, torch::Tensor kpe, torch::
   int words = 0;
   if (mask.has_value()) { CHECK_DT((*mask), at::kInt); TORCH_CHECK(mask->size(0) == T); words = mask->size(1); }
   c10::cuda::CUDAGuard g(q.device());
-  if (version == 2) {
+  if (version >= 2) {
     int64_t* tr = nullptr;
     int cap = 0;
     if (trace.has_value() && trace->defined()) {
@@ -269,9 +269,10 @@ void attn_prefill(torch::Tensor q, torch::Tensor kvb, torch::Tensor kpe, torch::
       tr = trace->data_ptr<int64_t>();
       cap = int((trace->numel() - 1) / 2);
     }
-    CK(cb::attn_prefill2(q.data_ptr(), kvb.data_ptr(), kpe.data_ptr(), T, H, tiles.data_ptr<int>(), tiles.size(0),
-                         ptr_or_null<const uint32_t>(mask), words, float(scale), out.data_ptr(),
-                         ptr_or_null<int>(status), cur_stream(), tr, cap, ptr_or_null<const float>(sink)));
+    auto fn = version == 3 ? cb::attn_prefill3 : cb::attn_prefill2;
+    CK(fn(q.data_ptr(), kvb.data_ptr(), kpe.data_ptr(), T, H, tiles.data_ptr<int>(), tiles.size(0),
+          ptr_or_null<const uint32_t>(mask), words, float(scale), out.data_ptr(), ptr_or_null<int>(status),
+          cur_stream(), tr, cap, ptr_or_null<const float>(sink)));
   } else {
     CK(cb::attn_prefill(q.data_ptr(), kvb.data_ptr(), kpe.data_ptr(), T, H, tiles.data_ptr<int>(), tiles.size(0),
                         ptr_or_null<const uint32_t>(mask), words, float(scale), out.data_ptr(),

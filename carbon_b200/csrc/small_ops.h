@@ -60,6 +60,9 @@ cudaError_t attn_prefill(const void* q, const void* kvb, const void* kpe, int T,
 cudaError_t attn_prefill2(const void* q, const void* kvb, const void* kpe, int T, int H, const int* tiles,
                           int n_tiles, const uint32_t* mask, int mask_words, float scale, void* out, int* status,
                           cudaStream_t s, int64_t* trace = nullptr, int trace_cap = 0, const float* sink = nullptr);
+cudaError_t attn_prefill3(const void* q, const void* kvb, const void* kpe, int T, int H, const int* tiles,
+                          int n_tiles, const uint32_t* mask, int mask_words, float scale, void* out, int* status,
+                          cudaStream_t s, int64_t* trace = nullptr, int trace_cap = 0, const float* sink = nullptr);
 
 // DSA indexer: logits GEMM with fused relu/weight/head-sum epilogue (gemm.cu) and exact top-k bitmask (topk.cu)
 cudaError_t indexer_logits(const void* keys, int L, const void* q, int Tq, int H, int Di, const float* w, float* out,

@@ -61,7 +61,7 @@ def mla_prefill(q: torch.Tensor, kvb: torch.Tensor, kpe: torch.Tensor, cu_seqlen
     elif key_masks is not None and any(m is not None for m in key_masks):
         mask = pack_key_mask(key_masks, cu_seqlens, q.device)
     out = torch.empty(T, H, 128, dtype=torch.bfloat16, device=q.device)
-    tiles = prefill_tiles(cu_seqlens, 256 if version == 2 else 128).to(q.device, non_blocking=True)
+    tiles = prefill_tiles(cu_seqlens, 256 if version >= 2 else 128).to(q.device, non_blocking=True)
     ext().attn_prefill(q.contiguous(), kvb.contiguous(), kpe.contiguous(), tiles, mask, float(scale), out, None,
                        version, trace, sink.float().contiguous() if sink is not None else None)
     return out

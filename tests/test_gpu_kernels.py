@@ -280,7 +280,7 @@ def test_mhc_kernels():
 # ----------------------------------------------------------------------------------------------------------------------
 # attention
 # ----------------------------------------------------------------------------------------------------------------------
-@pytest.mark.parametrize("version", [1, 2])
+@pytest.mark.parametrize("version", [1, 2, 3])
 @pytest.mark.parametrize("lens,masked,qscale", [([128], False, 1.0), ([300, 77, 5], False, 1.0), ([513], True, 1.0),
                                                 ([200, 260], True, 1.0), ([1000, 700], False, 4.0),
                                                 ([1300], True, 3.0), ([256, 384, 129], False, 1.0)])
@@ -288,7 +288,7 @@ def test_attn_prefill(lens, masked, qscale, version):
     _check_attn_prefill(lens, masked, qscale, version, with_sink=False)
 
 
-@pytest.mark.parametrize("version", [1, 2])
+@pytest.mark.parametrize("version", [1, 2, 3])
 @pytest.mark.parametrize("lens,masked", [([300, 77], False), ([513], True)])
 def test_attn_prefill_with_sink(lens, masked, version):
     _check_attn_prefill(lens, masked, 1.0, version, with_sink=True)
