@@ -194,6 +194,14 @@ def main():
         if world > 1:
             dist.barrier()
         torch.cuda.synchronize()
+        code = pctx.check() if hasattr(pctx, "check") else 0
+        if world > 1:                     # every rank learns of any rank's error, so all raise together
+            t = torch.tensor([code], device="cuda")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            code = int(t.item())
+        if code:
+            raise RuntimeError(f"rank {rank}: device collective error code {code} (peer wait timed out or buffer "
+                               "capacity exceeded)")
 
     # ---------------- prefill (device-timed) ----------------
     def prefill_step():

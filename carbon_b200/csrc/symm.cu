@@ -65,7 +65,10 @@ __global__ void p2p_barrier_kernel(const uint64_t* __restrict__ peer_flag_ptrs, 
   const uint32_t e = s_epoch;
   const int r = threadIdx.x;
   if (r < world) st_release_sys(reinterpret_cast<uint32_t*>(peer_flag_ptrs[r]) + my_rank, e);
-  if (r < world) {
+  // once an error is recorded the ranks are out of step: signal (so healthy peers are not held up) but do not
+  // wait, so that the failure surfaces at the next host check instead of every barrier waiting its full limit
+  const bool failed = status != nullptr && *reinterpret_cast<volatile int*>(status) != 0;
+  if (r < world && !failed) {
     const uint64_t t0 = globaltimer();
     uint32_t n = 0;
     while (int32_t(ld_acquire_sys(my_flags + r) - e) < 0) {

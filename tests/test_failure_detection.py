@@ -34,6 +34,11 @@ def test_barrier_times_out_with_status_and_context_survives():
     dt = time.time() - t0
     assert int(status.item()) == K_ERR_TIMEOUT_PEER
     assert 0.25 < dt < 10.0
+    # with an error already recorded, later barriers signal but do not wait: the failure surfaces at once
+    t1 = time.time()
+    e.p2p_barrier(peers, 0, epoch, flags, status, int(0.3e9))
+    torch.cuda.synchronize()
+    assert time.time() - t1 < 0.2
     x = torch.randn(256, 256, device="cuda")
     assert torch.isfinite(x @ x).all()          # context still usable
 
