@@ -665,9 +665,13 @@ __global__ void __launch_bounds__(384, 1) attn_prefill3_kernel(const __grid_cons
   uint64_t* r_full = bars + 1;                 // [NCH]
   uint64_t* r_empty = bars + 1 + NCH;          // [NCH]
   uint64_t* s_full = bars + 1 + 2 * NCH;       // [2 tiles][2 buffers]
-  uint64_t* p_full = bars + 5 + 2 * NCH;       // [2]
-  uint64_t* o_done = bars + 7 + 2 * NCH;       // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9 + 2 * NCH);
+  // P(j) ready, one barrier per S buffer: with double-buffered S the softmax of a tile can finish step j+1 before
+  // the MMA warp waits for step j, so a single barrier could be two phases ahead of its waiter (parity aliasing)
+  uint64_t* p_full = bars + 5 + 2 * NCH;       // [2 tiles][2 buffers]
+  // PV(j) done, also one barrier per step parity: the softmax can finish while PV(j-1) is still pending, so a
+  // single barrier could be two phases behind the PV that a waiter needs
+  uint64_t* o_done = bars + 9 + 2 * NCH;       // [2 tiles][2 step parities]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13 + 2 * NCH);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int4 tile = p.tiles[blockIdx.x];
@@ -686,7 +690,8 @@ __global__ void __launch_bounds__(384, 1) attn_prefill3_kernel(const __grid_cons
     mbar_init(q_full, 1);
     for (int i = 0; i < NCH; ++i) { mbar_init(&r_full[i], 1); mbar_init(&r_empty[i], 1); }
     for (int i = 0; i < 4; ++i) mbar_init(&s_full[i], 1);
-    for (int t = 0; t < 2; ++t) { mbar_init(&p_full[t], 128); mbar_init(&o_done[t], 1); }
+    for (int i = 0; i < 4; ++i) mbar_init(&p_full[i], 128);
+    for (int i = 0; i < 4; ++i) mbar_init(&o_done[i], 1);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -757,7 +762,7 @@ __global__ void __launch_bounds__(384, 1) attn_prefill3_kernel(const __grid_cons
             mma_f16_ts(tmem + 256 * t + 128 + 64 * half, pcol + 8 * k,
                        fa::desc_mn_sw128(v + k * 16 * 128, CH, 1024), id_pv, (j > 0 || k > 0) ? 1u : 0u);
         }
-        mma_commit(&o_done[t]);
+        mma_commit(&o_done[2 * t + (j & 1)]);
       };
       // prologue: the S of the first two steps of both tiles
       for (int j = 0; ok && j < 2 && j < n_kt; ++j) {
@@ -771,7 +776,7 @@ __global__ void __launch_bounds__(384, 1) attn_prefill3_kernel(const __grid_cons
         bool v_ready = false, k_ready = false;
         for (int t = 0; t < 2 && ok; ++t) {
           if (j >= n_kt_t[t]) continue;
-          if (!mbar_wait(&p_full[t], j & 1)) { fail(kErrTimeoutTmem); ok = false; break; }
+          if (!mbar_wait(&p_full[2 * t + (j & 1)], (j >> 1) & 1)) { fail(kErrTimeoutTmem); ok = false; break; }
           fa::trace_event(p, 1, t, j);
           tc_fence_after();
           if (!v_ready) { ok = wait_chunks(j * CH_PER_KV + 3, 2); v_ready = true; if (!ok) break; }
@@ -843,7 +848,9 @@ __global__ void __launch_bounds__(384, 1) attn_prefill3_kernel(const __grid_cons
       if (need && m_used != -INFINITY) alpha = fa::fast_exp2(m_used - m_ref);
       if (j > 0 && __any_sync(0xffffffffu, need)) {
         // O holds the sums of earlier steps at the old max: wait for the last PV, then rescale it in TMEM
-        if (!mbar_wait(&o_done[t], (j - 1) & 1)) { fail(kErrTimeoutTmem); ok = false; break; }
+        if (!mbar_wait(&o_done[2 * t + ((j - 1) & 1)], ((j - 1) >> 1) & 1)) {
+          fail(kErrTimeoutTmem); ok = false; break;
+        }
         tc_fence_after();
 #pragma unroll 1
         for (int c = 0; c < DV; c += 32) {
@@ -870,11 +877,11 @@ __global__ void __launch_bounds__(384, 1) attn_prefill3_kernel(const __grid_cons
       tmem_st_wait();
       tc_fence_before();
       if (tracer) fa::trace_event(p, 5, t, j);
-      mbar_arrive(&p_full[t]);
+      mbar_arrive(&p_full[2 * t + b]);
     }
     if (p.sink) l += fa::fast_exp2(p.sink[h] * 1.4426950408889634f - (m_used == -INFINITY ? 0.f : m_used));
     if (ok && nkt > 0) {
-      if (!mbar_wait(&o_done[t], (nkt - 1) & 1)) { fail(kErrTimeoutTmem); ok = false; }
+      if (!mbar_wait(&o_done[2 * t + ((nkt - 1) & 1)], ((nkt - 1) >> 1) & 1)) { fail(kErrTimeoutTmem); ok = false; }
     }
     if (ok && nkt > 0) {
       tc_fence_after();

@@ -16,6 +16,8 @@ cudaError_t p2p_gather_rows(const void* src, int n, int row_bytes, const uint64_
 cudaError_t p2p_scatter_partials(const void* part, int T, int D, const int* bounds_dev, int world, int my_rank,
                                  const uint64_t* slot_ptrs, int slot_rows, cudaStream_t s);
 cudaError_t reduce_slots(const void* slots, int world, int slot_rows, int n, int D, void* out, cudaStream_t s);
+cudaError_t p2p_a2a_heads(const void* src, const int* bounds_dev, int world, int my_rank, const uint64_t* dst_ptrs,
+                          int C, int mode, int max_rows, cudaStream_t s);
 cudaError_t moe_count(const int* ids, int Tk, int E, int world, int my_rank, const uint64_t* cnt_ptrs,
                       int* pair_rank, cudaStream_t s);
 cudaError_t moe_owner_layout(const int* cnt, int world, int El, int max_blocks, int* src_off, int* m_block_expert,
@@ -117,6 +119,12 @@ void p2p_scatter_partials(torch::Tensor part, torch::Tensor bounds, int64_t my_r
 void reduce_slots(torch::Tensor slots, int64_t world, int64_t slot_rows, int64_t n, torch::Tensor out) {
   CKP(cb::reduce_slots(slots.data_ptr(), world, slot_rows, n, out.size(1), out.data_ptr(), stream()));
 }
+void p2p_a2a_heads(torch::Tensor src, torch::Tensor bounds, int64_t my_rank, torch::Tensor dst_ptrs,
+                   int64_t block_bytes, int64_t mode, int64_t max_rows) {
+  TORCH_CHECK(src.is_cuda() && src.is_contiguous() && bounds.scalar_type() == at::kInt);
+  CKP(cb::p2p_a2a_heads(src.data_ptr(), bounds.data_ptr<int>(), dst_ptrs.numel(), my_rank, u64(dst_ptrs),
+                        block_bytes, mode, max_rows, stream()));
+}
 void moe_count(torch::Tensor ids, int64_t E, int64_t my_rank, torch::Tensor cnt_ptrs, torch::Tensor pair_rank) {
   TORCH_CHECK(ids.is_contiguous() && ids.scalar_type() == at::kInt);
   CKP(cb::moe_count(ids.data_ptr<int>(), ids.numel(), E, cnt_ptrs.numel(), my_rank, u64(cnt_ptrs),
@@ -177,6 +185,7 @@ void register_p2p(pybind11::module_& m) {
   m.def("p2p_gather_rows", &p2p_gather_rows);
   m.def("p2p_scatter_partials", &p2p_scatter_partials);
   m.def("reduce_slots", &reduce_slots);
+  m.def("p2p_a2a_heads", &p2p_a2a_heads);
   m.def("moe_count", &moe_count);
   m.def("moe_owner_layout", &moe_owner_layout);
   m.def("moe_dispatch", &moe_dispatch);

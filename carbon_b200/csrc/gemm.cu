@@ -56,7 +56,8 @@ static cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, con
                                const CUtensorMap& tsb, const GemmParams& p, int max_units, int num_sms,
                                cudaStream_t s) {
   using C = PairCfg<KIND, PAIR, EPI>;
-  constexpr int smem = gemm_pair_smem_bytes<KIND, PAIR, ST>();
+  constexpr int smem = gemm_pair_smem_bytes<KIND, PAIR, ST, EPI>();
+  static_assert(smem <= 227 * 1024, "pair GEMM shared memory above the per-CTA limit");
   auto kern = gemm_pair_kernel<KIND, EPI, PAIR, ST>;
   static int resident = 0;
   cudaLaunchAttribute attr[1];
@@ -377,7 +378,8 @@ cudaError_t gemm_fp8_scatter(const void* A, const void* B, const uint32_t* sfa, 
         !make_tmap_sf(&tsa, sfa, uint64_t(ceil_div(K, 512)) * ceil_div(M, 128), 1) ||
         !make_tmap_sf(&tsb, sfb, uint64_t(ceil_div(K, 512)) * ceil_div(N, 128), 2))
       return cudaErrorInvalidValue;
-    return launch_pair<KIND_MXF8, EPI_BF16_SCATTER, 2, 6>(ta, tb2, tsa, tsb, p, ceil_div(M, 256) * ceil_div(N, 256),
+    // five stages leave room for the epilogue's peer-store staging
+    return launch_pair<KIND_MXF8, EPI_BF16_SCATTER, 2, 5>(ta, tb2, tsa, tsb, p, ceil_div(M, 256) * ceil_div(N, 256),
                                                         num_sms, s);
   }
   return launch<KIND_MXF8, EPI_BF16_SCATTER, 128, 6, 2>(ta, tb, p, ceil_div(M, 128) * ceil_div(N, 128), num_sms, s);

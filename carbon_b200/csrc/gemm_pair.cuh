@@ -48,11 +48,16 @@ struct PairCfg {
   static constexpr int kThreads = 128 + 32 * kEpiWarps;
 };
 
-template <int KIND, int PAIR, int STAGES>
+// Peer-store staging of the scatter epilogue: per epilogue warp 32 rows x 64 bf16 columns, rows padded to 144 bytes
+// so that the row-per-lane writes (8 lanes per 16-byte phase) and the row-contiguous reads are bank-conflict free.
+constexpr int kScatterRowBytes = 144;
+constexpr int kScatterWarpBytes = 32 * kScatterRowBytes;
+
+template <int KIND, int PAIR, int STAGES, int EPI = EPI_BF16>
 constexpr int gemm_pair_smem_bytes() {
-  using C = PairCfg<KIND, PAIR, EPI_BF16>;
+  using C = PairCfg<KIND, PAIR, EPI>;
   return 1024 + STAGES * (C::TILE_A + C::TILE_B + C::SFA_BYTES + C::SFB_BYTES) + 8 * (2 * STAGES + 8) + 16 +
-         2 * 2 * 128 * 4;
+         2 * 2 * 128 * 4 + (EPI == EPI_BF16_SCATTER ? 16 + C::kEpiWarps * kScatterWarpBytes : 0);
 }
 
 template <int KIND, int EPI, int PAIR, int STAGES>
@@ -85,6 +90,7 @@ __global__ void __launch_bounds__(PairCfg<KIND, PAIR, EPI>::kThreads, 1)
   uint32_t* tmem_base_smem = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 8);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_smem + 1);
   float* xamax = reinterpret_cast<float*>(tmem_base_smem + 4);   // [2 tiles][2 halves][128 rows]
+  uint8_t* xstage = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(xamax + 2 * 2 * 128) + 15) & ~uintptr_t(15));
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
@@ -300,16 +306,56 @@ __global__ void __launch_bounds__(PairCfg<KIND, PAIR, EPI>::kThreads, 1)
       const bool ovl_first = C::kOvl > 0 && s == 0 && h == 1;       // stage 0: local columns [224,256)
       const bool ovl_owner = C::kOvl > 0 && ((s == 0 && h == 1) || (s == 1 && h == 0));
 
-      if constexpr (EPI == EPI_BF16 || EPI == EPI_BF16_SCATTER) {
-        __nv_bfloat16* row_base = nullptr;
-        if constexpr (EPI == EPI_BF16_SCATTER) {
+      if constexpr (EPI == EPI_BF16_SCATTER) {
+        // Rows go to their owners over NVLink.  A row-per-lane store would put 32 rows' 16-byte pieces into one
+        // warp instruction, i.e. 32 small NVLink writes; instead each 64-column slab of the warp's 32 rows is
+        // staged in shared memory and written back row-contiguous: one instruction covers four 128-byte row
+        // segments.  (Requires ldo % 8 == 0 and N % 8 == 0, checked by the host.)
+        uint8_t* stg = xstage + (warp - 4) * kScatterWarpBytes;
+        __nv_bfloat16* my_base = nullptr;
+        if (row_ok) {
           int r = 0;
           while (r + 1 < p.scatter_world && row >= p.scatter_bounds[r + 1]) ++r;
-          row_base = reinterpret_cast<__nv_bfloat16*>(p.scatter_ptrs[r]) +
-                     (size_t(p.scatter_rank) * p.scatter_rows + (row - p.scatter_bounds[r])) * size_t(p.ldo);
-        } else {
-          row_base = reinterpret_cast<__nv_bfloat16*>(p.out) + size_t(row) * p.ldo;
+          my_base = reinterpret_cast<__nv_bfloat16*>(p.scatter_ptrs[r]) +
+                    (size_t(p.scatter_rank) * p.scatter_rows + (row - p.scatter_bounds[r])) * size_t(p.ldo);
         }
+        const uint64_t my_base_u = reinterpret_cast<uint64_t>(my_base);
+#pragma unroll 1
+        for (int pp = 0; pp < 2; ++pp) {
+          const int slab = ovl_first ? 1 - pp : pp;          // ovl_first: the slab holding chunk 3 goes first
+#pragma unroll 1
+          for (int cc = 0; cc < 2; ++cc) {
+            const int c = 2 * slab + (ovl_first ? 1 - cc : cc);
+            const int lc = 128 * int(h) + 32 * c;
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(t_row + lc, v);
+            tmem_ld_wait();
+            if (pp == 0 && cc == 0 && ovl_owner) release(&tempty_ovl[s]);
+            uint4* d = reinterpret_cast<uint4*>(stg + lane * kScatterRowBytes + (c & 1) * 64);
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) {
+              uint4 w;
+              w.x = pack_bf16x2(__uint_as_float(v[8 * jj + 0]), __uint_as_float(v[8 * jj + 1]));
+              w.y = pack_bf16x2(__uint_as_float(v[8 * jj + 2]), __uint_as_float(v[8 * jj + 3]));
+              w.z = pack_bf16x2(__uint_as_float(v[8 * jj + 4]), __uint_as_float(v[8 * jj + 5]));
+              w.w = pack_bf16x2(__uint_as_float(v[8 * jj + 6]), __uint_as_float(v[8 * jj + 7]));
+              d[jj] = w;
+            }
+          }
+          __syncwarp();
+          const int col = nb * BN + 128 * int(h) + 64 * slab + 8 * int(lane & 7);
+#pragma unroll
+          for (int it = 0; it < 8; ++it) {
+            const int r = 4 * it + int(lane >> 3);
+            const uint64_t base = __shfl_sync(0xffffffffu, my_base_u, r);
+            const uint4 w = *reinterpret_cast<const uint4*>(stg + r * kScatterRowBytes + (lane & 7) * 16);
+            if (base != 0 && col < p.N) *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(base) + col) = w;
+          }
+          __syncwarp();
+        }
+        release(&tempty_full[s]);
+      } else if constexpr (EPI == EPI_BF16) {
+        __nv_bfloat16* row_base = reinterpret_cast<__nv_bfloat16*>(p.out) + size_t(row) * p.ldo;
 #pragma unroll 1
         for (int i = 0; i < 4; ++i) {
           const int c = ovl_first ? ((i + 3) & 3) : i;

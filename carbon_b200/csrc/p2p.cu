@@ -54,6 +54,45 @@ cudaError_t p2p_gather_rows(const void* src, int n, int row_bytes, const uint64_
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// head <-> token all-to-all around the decode attention core (tensor-parallel attention, `world` ranks own
+// contiguous token shards bounds[r]..bounds[r+1] and `C`-byte blocks of heads):
+//   mode 0, heads -> tokens: src [T, C] (all tokens, this rank's heads) -> peer d's [n_d, world * C] at column
+//           block my_rank, rows of d's tokens;
+//   mode 1, tokens -> heads: src [n_me, world * C] (this rank's tokens, all heads) -> peer d's [T, C] at the rows
+//           of this rank's tokens, column block d.
+// One CTA per (row, destination); every warp store writes 512 contiguous bytes of a destination row.
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void p2p_a2a_heads_kernel(const uint8_t* __restrict__ src, const int* __restrict__ bounds, int world,
+                                     int my_rank, const uint64_t* __restrict__ dst_ptrs, int C, int mode) {
+  const int i = blockIdx.x, d = blockIdx.y;
+  const uint8_t* s;
+  uint8_t* t;
+  if (mode == 0) {
+    const int lo = bounds[d], n = bounds[d + 1] - lo;
+    if (i >= n) return;
+    s = src + size_t(lo + i) * C;
+    t = reinterpret_cast<uint8_t*>(dst_ptrs[d]) + (size_t(i) * world + my_rank) * C;
+  } else {
+    const int lo = bounds[my_rank], n = bounds[my_rank + 1] - lo;
+    if (i >= n) return;
+    s = src + (size_t(i) * world + d) * C;
+    t = reinterpret_cast<uint8_t*>(dst_ptrs[d]) + size_t(lo + i) * C;
+  }
+  for (int c = threadIdx.x; c < C / 16; c += blockDim.x)
+    reinterpret_cast<uint4*>(t)[c] = reinterpret_cast<const uint4*>(s)[c];
+  __threadfence_system();
+}
+
+cudaError_t p2p_a2a_heads(const void* src, const int* bounds_dev, int world, int my_rank, const uint64_t* dst_ptrs,
+                          int C, int mode, int max_rows, cudaStream_t s) {
+  if (max_rows <= 0) return cudaSuccess;
+  if (C % 16 || (mode != 0 && mode != 1)) return cudaErrorInvalidValue;
+  p2p_a2a_heads_kernel<<<dim3(max_rows, world), 256, 0, s>>>(reinterpret_cast<const uint8_t*>(src), bounds_dev,
+                                                             world, my_rank, dst_ptrs, C, mode);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------------------------------
 // reduce-scatter: partial [T, D] bf16 -> owner r's slot buffer rows [my_rank][i] for rows of r's shard;
 // reduce_slots: out[i] = sum_s slots[s][i] (fp32 accumulate, bf16 out)
 // ---------------------------------------------------------------------------------------------------------------
@@ -121,15 +160,20 @@ cudaError_t reduce_slots(const void* slots, int world, int slot_rows, int n, int
 // count matrix cnt_ptrs[owner] -> int32 [world(src)][E_local].
 __global__ void moe_count_kernel(const int* __restrict__ ids, int Tk, int El, int my_rank,
                                  const uint64_t* __restrict__ cnt_ptrs, int* __restrict__ pair_rank) {
+  constexpr int kPer = 8;                  // consecutive pairs per thread per pass
   __shared__ int sw[32];
   const int e = blockIdx.x;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   int base = 0;
-  for (int i0 = 0; i0 < Tk; i0 += blockDim.x) {
-    const int i = i0 + threadIdx.x;
-    const int hit = (i < Tk && ids[i] == e) ? 1 : 0;
-    // inclusive block scan of hit
-    int v = hit;
-    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int i0 = 0; i0 < Tk; i0 += blockDim.x * kPer) {
+    const int b0 = i0 + threadIdx.x * kPer;
+    uint32_t mask = 0;
+#pragma unroll
+    for (int u = 0; u < kPer; ++u)
+      if (b0 + u < Tk && ids[b0 + u] == e) mask |= 1u << u;
+    const int hits = __popc(mask);
+    // inclusive block scan of hits
+    int v = hits;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
       const int n = __shfl_up_sync(0xffffffffu, v, o);
@@ -147,8 +191,12 @@ __global__ void moe_count_kernel(const int* __restrict__ ids, int Tk, int El, in
       if (lane < nw) sw[lane] = x;
     }
     __syncthreads();
-    const int incl = v + (wid > 0 ? sw[wid - 1] : 0);
-    if (hit) pair_rank[i] = base + incl - 1;
+    int r = base + v + (wid > 0 ? sw[wid - 1] : 0) - hits;
+    while (mask) {
+      const int u = __ffs(mask) - 1;
+      mask &= mask - 1;
+      pair_rank[b0 + u] = r++;
+    }
     base += sw[nw - 1];
     __syncthreads();
   }
@@ -207,6 +255,7 @@ __global__ void moe_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int D, 
   const int t = blockIdx.x;
   const int row_blocks = cap / 128;
   __shared__ int s_dst[16], s_owner[16];
+  __shared__ uint32_t s_sf[64];            // UE8M0 scale of each 128-column block, four per word
   if (threadIdx.x < k) {
     const int e = ids[t * k + threadIdx.x];
     const int owner = e / El, el = e % El;
@@ -217,8 +266,10 @@ __global__ void moe_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int D, 
     s_owner[threadIdx.x] = owner;
     pos_out[t * k + threadIdx.x] = row;
   }
+  if (threadIdx.x < 64) s_sf[threadIdx.x] = 0x7f7f7f7fu;
   __syncthreads();
-  // each group of 16 threads quantises one 128-column block (8 values per thread)
+  // each group of 16 threads quantises one 128-column block (8 values per thread); every warp store writes 256
+  // contiguous bytes of a destination row
   for (int col = threadIdx.x * 8; col < D; col += blockDim.x * 8) {
     const uint4 raw = *reinterpret_cast<const uint4*>(x + size_t(t) * D + col);
     float v[8] = {bf16_lo(raw.x), bf16_hi(raw.x), bf16_lo(raw.y), bf16_hi(raw.y),
@@ -234,18 +285,25 @@ __global__ void moe_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int D, 
     q.x = pack_fp8x4(v[0] * inv, v[1] * inv, v[2] * inv, v[3] * inv);
     q.y = pack_fp8x4(v[4] * inv, v[5] * inv, v[6] * inv, v[7] * inv);
     const int kb = col / 128;
+    if ((threadIdx.x & 15) == 0) reinterpret_cast<uint8_t*>(s_sf)[kb] = uint8_t(sb);
     for (int j = 0; j < k; ++j) {
       const int row = s_dst[j];
       if (row < 0) continue;
       uint8_t* dst = reinterpret_cast<uint8_t*>(recv_ptrs[s_owner[j]]) + size_t(row) * D + col;
       *reinterpret_cast<uint2*>(dst) = q;
-      if ((threadIdx.x & 15) == 0) {
-        const int rb = row >> 7, r = row & 127;
-        uint8_t* sfb = reinterpret_cast<uint8_t*>(sf_ptrs[s_owner[j]]) +
-                       ((size_t(kb >> 2) * row_blocks + rb) * 128 + (r & 31) * 4 + (r >> 5)) * 4 + (kb & 3);
-        *sfb = uint8_t(sb);
-      }
     }
+  }
+  __syncthreads();
+  // scale words: word g of a row holds the scales of column blocks 4g..4g+3 (SF tile layout of the owner)
+  const int words = (D / 128 + 3) / 4;
+  for (int i = threadIdx.x; i < k * words; i += blockDim.x) {
+    const int j = i / words, g = i - j * words;
+    const int row = s_dst[j];
+    if (row < 0) continue;
+    const int rb = row >> 7, r = row & 127;
+    uint32_t* sfw = reinterpret_cast<uint32_t*>(sf_ptrs[s_owner[j]]) +
+                    (size_t(g) * row_blocks + rb) * 128 + (r & 31) * 4 + (r >> 5);
+    *sfw = s_sf[g];
   }
   __threadfence_system();
 }
@@ -254,51 +312,68 @@ cudaError_t moe_dispatch(const void* x, int T, int D, const int* ids, int k, int
                          const int* pair_rank, const uint64_t* recv_ptrs, const uint64_t* sf_ptrs,
                          const uint64_t* off_ptrs, int cap, int* pos_out, int* status, cudaStream_t s) {
   if (T == 0) return cudaSuccess;
-  if (D % 128 || k > 16 || cap % 128) return cudaErrorInvalidValue;
+  if (D % 128 || D > 64 * 512 || k > 16 || cap % 128) return cudaErrorInvalidValue;
   moe_dispatch_kernel<<<T, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), D, ids, k, El, my_rank, pair_rank,
                                         recv_ptrs, sf_ptrs, off_ptrs, cap, pos_out, status);
   return cudaGetLastError();
 }
 
 // Combine: out[t] = add[t] + sum_j w[t,j] * y_owner(j)[pos[t,j]] — P2P loads from the owners' output buffers.
+// The k remote loads of a column chunk are issued together (KMAX unrolled, predicated) so that each thread keeps k
+// NVLink reads in flight instead of one.
+template <int KMAX>
 __global__ void moe_combine_pull_kernel(const uint64_t* __restrict__ y_ptrs, int D, const int* __restrict__ ids,
                                         const int* __restrict__ pos, const float* __restrict__ w, int k, int El,
                                         const __nv_bfloat16* __restrict__ add, __nv_bfloat16* __restrict__ out) {
   const int t = blockIdx.x;
-  for (int c = threadIdx.x * 8; c < D; c += blockDim.x * 8) {
+  __shared__ const uint4* s_src[KMAX];
+  __shared__ float s_w[KMAX];
+  if (threadIdx.x < KMAX) {
+    const int j = threadIdx.x;
+    const int row = j < k ? pos[t * k + j] : -1;
+    s_src[j] = row < 0 ? nullptr
+                       : reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(
+                                                            y_ptrs[ids[t * k + j] / El]) + size_t(row) * D);
+    s_w[j] = row < 0 ? 0.f : w[t * k + j];
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < D / 8; c += blockDim.x) {
     float acc[8];
     if (add) {
-      const uint4 a = *reinterpret_cast<const uint4*>(add + size_t(t) * D + c);
+      const uint4 a = *reinterpret_cast<const uint4*>(add + size_t(t) * D + 8 * c);
       acc[0] = bf16_lo(a.x); acc[1] = bf16_hi(a.x); acc[2] = bf16_lo(a.y); acc[3] = bf16_hi(a.y);
       acc[4] = bf16_lo(a.z); acc[5] = bf16_hi(a.z); acc[6] = bf16_lo(a.w); acc[7] = bf16_hi(a.w);
     } else {
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[j] = 0.f;
     }
-    for (int j = 0; j < k; ++j) {
-      const int row = pos[t * k + j];
-      if (row < 0) continue;
-      const int owner = ids[t * k + j] / El;
-      const float wv = w[t * k + j];
-      const uint4 v = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(y_ptrs[owner]) +
-                                                      size_t(row) * D + c);
-      acc[0] += wv * bf16_lo(v.x); acc[1] += wv * bf16_hi(v.x); acc[2] += wv * bf16_lo(v.y);
-      acc[3] += wv * bf16_hi(v.y); acc[4] += wv * bf16_lo(v.z); acc[5] += wv * bf16_hi(v.z);
-      acc[6] += wv * bf16_lo(v.w); acc[7] += wv * bf16_hi(v.w);
+    uint4 v[KMAX];
+#pragma unroll
+    for (int j = 0; j < KMAX; ++j) v[j] = s_src[j] ? s_src[j][c] : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int j = 0; j < KMAX; ++j) {
+      const float wv = s_w[j];
+      acc[0] += wv * bf16_lo(v[j].x); acc[1] += wv * bf16_hi(v[j].x); acc[2] += wv * bf16_lo(v[j].y);
+      acc[3] += wv * bf16_hi(v[j].y); acc[4] += wv * bf16_lo(v[j].z); acc[5] += wv * bf16_hi(v[j].z);
+      acc[6] += wv * bf16_lo(v[j].w); acc[7] += wv * bf16_hi(v[j].w);
     }
     uint4 o;
     o.x = pack_bf16x2(acc[0], acc[1]); o.y = pack_bf16x2(acc[2], acc[3]);
     o.z = pack_bf16x2(acc[4], acc[5]); o.w = pack_bf16x2(acc[6], acc[7]);
-    *reinterpret_cast<uint4*>(out + size_t(t) * D + c) = o;
+    *reinterpret_cast<uint4*>(out + size_t(t) * D + 8 * c) = o;
   }
 }
 
 cudaError_t moe_combine_pull(const uint64_t* y_ptrs, int T, int D, const int* ids, const int* pos, const float* w,
                              int k, int El, const void* add, void* out, cudaStream_t s) {
   if (T == 0) return cudaSuccess;
-  moe_combine_pull_kernel<<<T, 128, 0, s>>>(y_ptrs, D, ids, pos, w, k, El,
-                                            reinterpret_cast<const __nv_bfloat16*>(add),
-                                            reinterpret_cast<__nv_bfloat16*>(out));
+  if (D % 8 || k > 16) return cudaErrorInvalidValue;
+  const auto* a = reinterpret_cast<const __nv_bfloat16*>(add);
+  auto* o = reinterpret_cast<__nv_bfloat16*>(out);
+  if (k <= 8)
+    moe_combine_pull_kernel<8><<<T, 128, 0, s>>>(y_ptrs, D, ids, pos, w, k, El, a, o);
+  else
+    moe_combine_pull_kernel<16><<<T, 128, 0, s>>>(y_ptrs, D, ids, pos, w, k, El, a, o);
   return cudaGetLastError();
 }
 

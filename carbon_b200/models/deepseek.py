@@ -209,6 +209,7 @@ class DeepseekModel:
         wo = get(a + "wo.weight")                                                  # [D, H*dv]
         L.wo = Lin(wo[:, h0 * dv:h1 * dv].contiguous(), dev, self.fp8)
         L.sink = get(a + "sink")[h0:h1].float().contiguous() if cfg.attn_sink else None
+        L.sink_all = get(a + "sink").float().contiguous().to(dev) if cfg.attn_sink else None     # every head
         L.has_indexer = cfg.has_indexer(i)
         if L.has_indexer:
             ix = a + "indexer."
@@ -407,7 +408,12 @@ class DeepseekModel:
         with region("attn.absorb_q"):
             q_abs = head_bmm(q[..., :dn], L.w_uk)                                    # [T, Hl, r]
             qf = torch.cat([q_abs.to(self.act_dtype), q[..., dn:].to(self.act_dtype)], dim=-1).contiguous()
-        idx = fb.key_slots[lo:hi] if dp else fb.key_slots
+        # Tensor-parallel heads, but the core runs token-parallel: every rank would otherwise stream the selected
+        # latent rows of ALL tokens for its few heads.  Two small all-to-alls (q in, o_lat out) let each rank read
+        # only its own tokens' rows, for every head.
+        swap = not dp and pc.world > 1 and hasattr(pc, "heads_to_tokens")
+        local = dp or swap
+        idx = fb.key_slots[lo:hi] if local else fb.key_slots
         src = cfg.index_source(i)
         if src is not None and int(fb.key_slots.shape[1]) > cfg.index_topk:
             if src == i:
@@ -415,12 +421,19 @@ class DeepseekModel:
                     qi, _, wi = idx_l
                     sel = A.indexer_topk(qi, wi, cache.index_k[i], fb.key_slots[lo:hi].contiguous(),
                                          fb.n_keys[lo:hi].contiguous(), cfg.index_topk)
-                    idx = sel if dp else pc.gather_rows(sel)
+                    idx = sel if local else pc.gather_rows(sel)
                 self._dsa[i] = idx
             else:
                 idx = self._dsa[src]                # selection shared with the index-source layer
-        with region("attn.core_decode"):
-            o_lat = A.sparse_mla(qf, cache.latent[i], idx.contiguous(), cfg.softmax_scale, r, sink=L.sink)
+        if swap:
+            with region("attn.core_decode"):
+                q_tok = pc.heads_to_tokens(qf)                                      # [n_r, H, r + dr]
+                o_tok = A.sparse_mla(q_tok, cache.latent[i], idx.contiguous(), cfg.softmax_scale, r,
+                                     sink=L.sink_all)
+                o_lat = pc.tokens_to_heads(o_tok)                                   # [T, Hl, r]
+        else:
+            with region("attn.core_decode"):
+                o_lat = A.sparse_mla(qf, cache.latent[i], idx.contiguous(), cfg.softmax_scale, r, sink=L.sink)
         with region("attn.absorb_o"):
             return head_bmm(o_lat, L.w_uv)                                           # [T, Hl, dv]
 

@@ -99,6 +99,26 @@ class DistCtx(ParallelCtx):
         dist.all_to_all_single(out, x.contiguous(), recv_counts, send_counts, group=self.group)
         return out
 
+    def heads_to_tokens(self, x: torch.Tensor) -> torch.Tensor:
+        """Tensor-parallel head shard of every token [T, Hl, W] -> every head of this rank's tokens
+        [n_r, world * Hl, W] (head blocks in rank order)."""
+        T, Hl, W = x.shape
+        cnt = self.counts()
+        n = cnt[self.rank]
+        out = x.new_empty((self.world * n, Hl, W))
+        dist.all_to_all_single(out, x.contiguous(), [n] * self.world, cnt, group=self.group)
+        return out.view(self.world, n, Hl, W).permute(1, 0, 2, 3).reshape(n, self.world * Hl, W)
+
+    def tokens_to_heads(self, y: torch.Tensor) -> torch.Tensor:
+        """Inverse of ``heads_to_tokens``: [n_r, world * Hl, W] -> [T, Hl, W]."""
+        n, HW, W = y.shape
+        Hl = HW // self.world
+        cnt = self.counts()
+        send = y.view(n, self.world, Hl, W).permute(1, 0, 2, 3).reshape(self.world * n, Hl, W)
+        out = y.new_empty((sum(cnt), Hl, W))
+        dist.all_to_all_single(out, send.contiguous(), cnt, [n] * self.world, group=self.group)
+        return out
+
     def exchange_counts(self, send_counts: torch.Tensor) -> List[int]:
         """send_counts [world] int64 (this rank -> r) -> recv_counts (r -> this rank)."""
         recv = torch.empty_like(send_counts)

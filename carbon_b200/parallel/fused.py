@@ -93,6 +93,28 @@ class FusedCtx(DistCtx):
             self._bounds_key = key
         return self._bounds_dev
 
+    def heads_to_tokens(self, x: torch.Tensor) -> torch.Tensor:
+        """[T, Hl, W] (all tokens, this rank's heads) -> [n_r, world * Hl, W]: P2P stores of each owner's token rows
+        into column block `rank` of its buffer, one barrier."""
+        T, Hl, W = x.shape
+        cnt = self.counts()
+        buf = self._gbuf("h2t", (self.world * Hl, W), x.dtype, max(cnt))
+        ext().p2p_a2a_heads(x.contiguous(), self._bounds_tensor(), self.rank, buf.peers, Hl * W * x.element_size(), 0,
+                            max(cnt))
+        self.barrier()
+        return buf.local[: cnt[self.rank]]
+
+    def tokens_to_heads(self, y: torch.Tensor) -> torch.Tensor:
+        """Inverse of ``heads_to_tokens``: [n_r, world * Hl, W] -> [T, Hl, W]."""
+        n, HW, W = y.shape
+        Hl = HW // self.world
+        T = self.bounds[-1] - self.bounds[0]
+        buf = self._gbuf("t2h", (Hl, W), y.dtype, T)
+        ext().p2p_a2a_heads(y.contiguous(), self._bounds_tensor(), self.rank, buf.peers, Hl * W * y.element_size(), 1,
+                            n)
+        self.barrier()
+        return buf.local[:T]
+
     def reduce_scatter_rows(self, x: torch.Tensor) -> torch.Tensor:
         T, D = x.shape
         buf = self._rs_buf(D)

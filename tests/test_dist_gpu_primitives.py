@@ -43,9 +43,9 @@ def _worker(rank, world, port, q):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
     res = {}
     try:
-        f = FusedCtx(rank, world, heap_bytes=1 << 30, max_tokens=512, max_seq=256)
+        f = FusedCtx(rank, world, heap_bytes=2 << 30, max_tokens=4608, max_seq=256)
         d = DistCtx(rank, world)
-        bounds = [0, 100, 230]
+        bounds = [0, 100, 230] if world == 2 else [0, 230]
         f.set_bounds(bounds)
         d.set_bounds(bounds)
         lo, hi = bounds[rank], bounds[rank + 1]
@@ -84,6 +84,17 @@ def _worker(rank, world, port, q):
         h = torch.randn(hi - lo, mcfg.hidden_size, device=dev, generator=g).to(torch.bfloat16)
         w, idx = C.router_topk(torch.randn(hi - lo, 8, device=dev, generator=g), None, 2, "sigmoid", 1.0, True)
         res["moe"] = _rel(f.moe(model, L, h, w, idx, None), d.moe(model, L, h, w, idx, None))
+        # prefill-sized shards: CTA-pair o_proj scatter epilogue (M >= 512) and the two-chunk pipelined MoE
+        big = [0, 2300, 4608] if world == 2 else [0, 4608]
+        f.set_bounds(big)
+        d.set_bounds(big)
+        blo, bhi = big[rank], big[rank + 1]
+        o = torch.randn(4608, 2048, device=dev, generator=g).to(torch.bfloat16)
+        res["gemm_rs_big"] = _rel(f.row_parallel_out(lin, o), d.reduce_scatter_rows(lin(o)))
+        h = torch.randn(bhi - blo, mcfg.hidden_size, device=dev, generator=g).to(torch.bfloat16)
+        w, idx = C.router_topk(torch.randn(bhi - blo, 8, device=dev, generator=g), None, 2, "sigmoid", 1.0, True)
+        sh = torch.randn(bhi - blo, mcfg.hidden_size, device=dev, generator=g).to(torch.bfloat16)
+        res["moe_big"] = _rel(f.moe(model, L, h, w, idx, sh), d.moe(model, L, h, w, idx, sh))
         torch.cuda.synchronize()
         res["status"] = f.check()
         q.put((rank, res))
@@ -95,21 +106,30 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_fused_collectives_match_nccl():
+def _run(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    ps = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    ps = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in ps:
         p.start()
-    res = dict(q.get(timeout=300) for _ in range(2))
+    res = dict(q.get(timeout=300) for _ in range(world))
     for p in ps:
         p.join(timeout=60)
     for rank, r in res.items():
         assert "error" not in r, (rank, r)
         assert r["status"] == 0, (rank, r)
         assert r["gather_bf16"] == 0 and r["gather_i32"] == 0, (rank, r)
-        assert r["rs"] < 1e-2 and r["gemm_rs"] < 1e-2, (rank, r)
+        assert r["rs"] < 1e-2 and r["gemm_rs"] < 1e-2 and r["gemm_rs_big"] < 1e-2, (rank, r)
         assert r["embed"] == 0 and r["embed_vs_table"] == 0, (rank, r)
-        assert r["moe"] < 2e-2, (rank, r)
+        assert r["moe"] < 2e-2 and r["moe_big"] < 2e-2, (rank, r)
+
+
+def test_fused_collectives_one_rank():
+    """The same kernels with every peer pointer local: dispatch / combine / scatter index arithmetic on one GPU."""
+    _run(1)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fused_collectives_match_nccl():
+    _run(2)
