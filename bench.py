@@ -189,6 +189,13 @@ def main():
     torch.cuda.synchronize()
     init_s = time.time() - t0
     gen = torch.Generator().manual_seed(1234)     # SPMD: every rank builds the same requests
+    t_start = time.time()
+
+    def phase(name):                      # progress on stderr: a stalled run shows where it stopped
+        if rank == 0:
+            print(f"[bench] {time.time() - t_start:8.1f}s {name}", file=sys.stderr, flush=True)
+
+    phase(f"engine ready (init {init_s:.1f}s)")
 
     def barrier():
         if world > 1:
@@ -211,9 +218,11 @@ def main():
             eng.release(r)
         return logits
 
-    for _ in range(args.warmup):
+    for w_ in range(args.warmup):
         prefill_step()
+        phase(f"prefill warm-up {w_ + 1}/{args.warmup}")
     barrier()
+    phase("prefill timed")
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
     with ClockSampler(local) as clk:
         ev[0].record()
@@ -225,6 +234,7 @@ def main():
     pf_ms = max_over_ranks(pf_ms, world)
 
     # ---------------- prefill end to end through the public API (H2D ids from pinned host, D2H next tokens) ------
+    phase("prefill end-to-end")
     host_ids = [torch.randint(0, cfg.vocab_size, (S,), generator=gen).pin_memory() for _ in range(P)]
     barrier()
     ee = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
@@ -252,10 +262,12 @@ def main():
     def next_ids():
         return torch.randint(0, cfg.vocab_size, (B,), generator=gen).tolist()
 
+    phase("decode warm-up (graph capture)")
     for _ in range(args.warmup):
         for _ in range(2):
             eng.decode(reqs, next_ids())
     barrier()
+    phase("decode timed")
     step_ms = []
     for _ in range(args.steps):
         for _ in range(args.decode_steps):

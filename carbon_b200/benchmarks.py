@@ -82,7 +82,7 @@ def bench_attn(a):
     ms = time_fn(lambda: mla_prefill(q, kvb, kpe, cu, 192 ** -0.5, mask, version=a.attn_version), iters=5)
     flops = B * H * (S * S / 2) * (192 + 128) * 2
     pk = peaks()
-    res.update({"bench": "mla_prefill_attention", "kernel_version": a.attn_version, "batch": B, "seq": S, "heads": H, "dsa": a.dsa, "ms": round(ms, 3),
+    res.update({"bench": "mla_prefill_attention", "kernel_version": a.attn_version or (3 if a.dsa else 2), "batch": B, "seq": S, "heads": H, "dsa": a.dsa, "ms": round(ms, 3),
                 "tflops": round(flops / ms / 1e9, 1),
                 "frac_of_bf16_peak": round(flops / ms / 1e9 / pk["bf16_tflops"], 3), "peak_src": pk["src"],
                 "flops_counted": "dense causal (masked DSA keys still cost a full tile)"})
@@ -239,7 +239,7 @@ def main(argv=None):
     ap.add_argument("--k", type=int, default=7168)
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--hidden", type=int, default=7168)
-    ap.add_argument("--attn-version", type=int, default=2,
+    ap.add_argument("--attn-version", type=int, default=0,
                     help="attn: 3 = two Q tiles, 64-key steps, double-buffered S; 2 = two Q tiles, 128-key steps; 1 = one")
     ap.add_argument("--pair", type=int, default=-1, help="gemm: -1 auto, 1 CTA-pair 256x256 tiles, 0 128x128 tiles")
     a = ap.parse_args(argv)

@@ -517,6 +517,17 @@ __global__ void __launch_bounds__(384, 1) attn_prefill2_kernel(const __grid_cons
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     const bool tracer = (q == 0 && lane == 0);
+    // DSA mask words of a step are fetched one step ahead, off the softmax's critical path
+    const bool use_mask = p.mask != nullptr && qi < seq_len;
+    auto load_mask = [&](int jj, uint32_t (&w)[4]) {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int wi = ((jj * BN) >> 5) + c;
+        w[c] = wi < p.mask_words ? __ldg(p.mask + size_t(tok) * p.mask_words + wi) : 0u;
+      }
+    };
+    uint32_t mwn[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
+    if (use_mask && nkt > 0) load_mask(0, mwn);
     for (int j = 0; j < nkt; ++j) {
       if (tracer) fa::trace_event(p, 3, t, j);
       if (!mbar_wait(&s_full[t], j & 1)) { fail(kErrTimeoutTmem); ok = false; break; }
@@ -536,14 +547,8 @@ __global__ void __launch_bounds__(384, 1) attn_prefill2_kernel(const __grid_cons
       }
       const int k0 = j * BN;
       float mt = -INFINITY;
-      uint32_t mw[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
-      if (p.mask && qi < seq_len) {
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int wi = (k0 >> 5) + c;
-          mw[c] = wi < p.mask_words ? p.mask[size_t(tok) * p.mask_words + wi] : 0u;
-        }
-      }
+      uint32_t mw[4] = {mwn[0], mwn[1], mwn[2], mwn[3]};
+      if (use_mask && j + 1 < nkt) load_mask(j + 1, mwn);    // next step's words load under this step's work
       // no per-key work when every row of the warp sees all 128 keys (below the diagonal, mask words all ones:
       // e.g. DSA rows with fewer candidates than top-k)
       const bool full_row = (k0 + BN - 1 <= qi) && ((mw[0] & mw[1] & mw[2] & mw[3]) == 0xffffffffu);
@@ -805,6 +810,15 @@ __global__ void __launch_bounds__(384, 1) attn_prefill3_kernel(const __grid_cons
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
     const bool tracer = (q == 0 && lane == 0);
+    // DSA mask words of a step are fetched one step ahead, off the softmax's critical path
+    const bool use_mask = p.mask != nullptr && qi < seq_len;
+    auto load_mask = [&](int jj, uint32_t& w0, uint32_t& w1) {
+      const int wi = (jj * BN) >> 5;
+      w0 = wi < p.mask_words ? __ldg(p.mask + size_t(tok) * p.mask_words + wi) : 0u;
+      w1 = wi + 1 < p.mask_words ? __ldg(p.mask + size_t(tok) * p.mask_words + wi + 1) : 0u;
+    };
+    uint32_t mwn0 = 0xffffffffu, mwn1 = 0xffffffffu;
+    if (use_mask && nkt > 0) load_mask(0, mwn0, mwn1);
     for (int j = 0; j < nkt; ++j) {
       const int b = j & 1;
       if (tracer) fa::trace_event(p, 3, t, j);
@@ -820,12 +834,8 @@ __global__ void __launch_bounds__(384, 1) attn_prefill3_kernel(const __grid_cons
         tmem_ld_wait();
       }
       const int k0 = j * BN;
-      uint32_t mw0 = 0xffffffffu, mw1 = 0xffffffffu;
-      if (p.mask && qi < seq_len) {
-        const int wi = k0 >> 5;
-        mw0 = wi < p.mask_words ? p.mask[size_t(tok) * p.mask_words + wi] : 0u;
-        mw1 = wi + 1 < p.mask_words ? p.mask[size_t(tok) * p.mask_words + wi + 1] : 0u;
-      }
+      const uint32_t mw0 = mwn0, mw1 = mwn1;
+      if (use_mask && j + 1 < nkt) load_mask(j + 1, mwn0, mwn1);   // next step's words load under this step
       const bool full_row = (k0 + BN - 1 <= qi) && ((mw0 & mw1) == 0xffffffffu);
       float pm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
       if (__all_sync(0xffffffffu, full_row)) {

@@ -24,7 +24,7 @@ from ._ext import ext
 
 
 def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens: List[int], scale: float,
-                      key_masks=None, version: int = 2, trace: Optional[torch.Tensor] = None,
+                      key_masks=None, version: int = 0, trace: Optional[torch.Tensor] = None,
                       sink: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Reference-layout entry: q [T,H,dqk], k [T,H,dqk], v [T,H,dv]; sink [H]: per-head attention-sink logit."""
     T, H, dv = q.shape[0], q.shape[1], v.shape[2]
@@ -45,11 +45,13 @@ def prefill_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seql
 
 
 def mla_prefill(q: torch.Tensor, kvb: torch.Tensor, kpe: torch.Tensor, cu_seqlens: List[int], scale: float,
-                key_masks=None, version: int = 2, trace: Optional[torch.Tensor] = None,
+                key_masks=None, version: int = 0, trace: Optional[torch.Tensor] = None,
                 sink: Optional[torch.Tensor] = None) -> torch.Tensor:
     """MLA prefill in the projection's own layout: q [T,H,192], kvb [T,H,256] = (k_nope | v) straight from the
     wkv_b GEMM, kpe [T,64] the shared RoPE key (k = [k_nope, kpe] per head). Returns o [T,H,128].
-    version 2: two 128-row Q tiles per CTA sharing each K/V tile (the default); 1: one Q tile per CTA."""
+    version 1: one 128-row Q tile per CTA; 2: two Q tiles per CTA sharing each 128-key K/V tile; 3: two Q tiles,
+    64-key steps with double-buffered S.  0 (default) picks by measurement on B200: 3 for DSA-masked calls (its
+    shorter steps keep the masked softmax off the tensor pipe's critical path), 2 for dense causal ones."""
     T, H = q.shape[0], q.shape[1]
     if not q.is_cuda:
         dn = q.shape[2] - kpe.shape[-1]
@@ -60,6 +62,8 @@ def mla_prefill(q: torch.Tensor, kvb: torch.Tensor, kpe: torch.Tensor, cu_seqlen
         mask = key_masks
     elif key_masks is not None and any(m is not None for m in key_masks):
         mask = pack_key_mask(key_masks, cu_seqlens, q.device)
+    if version == 0:
+        version = 3 if mask is not None else 2
     out = torch.empty(T, H, 128, dtype=torch.bfloat16, device=q.device)
     tiles = prefill_tiles(cu_seqlens, 256 if version >= 2 else 128).to(q.device, non_blocking=True)
     ext().attn_prefill(q.contiguous(), kvb.contiguous(), kpe.contiguous(), tiles, mask, float(scale), out, None,
