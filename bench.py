@@ -345,7 +345,7 @@ def heap_bytes(cfg, world, max_tokens, max_seq):
     cap = int(max_local * cfg.n_activated_experts * 1.6) + (cfg.n_routed_experts // world) * 256 + 256
     cap2 = int((max_local + 1) // 2 * cfg.n_activated_experts * 1.6) + (cfg.n_routed_experts // world) * 256 + 256
     moe = (cap + cap2) * (D * 3 + D // 32) + (2 << 20)       # buffer sets of a whole call and of a second chunk
-    width = cfg.q_lora_rank + cfg.kv_lora_rank + cfg.qk_rope_head_dim + cfg.index_head_dim
+    width = cfg.q_lora_rank + cfg.latent_dim + cfg.index_head_dim
     gathers = 2 * 2 * max_tokens * (width * 2 + (max_seq // 32 + 1) * 4 + cfg.index_topk * 4)
     emb = (cfg.vocab_size // world + 1) * D * 2
     return int(rs + moe + gathers + emb + (1 << 30))

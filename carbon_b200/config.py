@@ -46,6 +46,22 @@ class ModelConfig:
     index_sources: tuple = ()
     # per-head learned attention sink: one extra logit in each softmax denominator (attn.sink [n_heads] fp32)
     attn_sink: bool = False
+    # attention kind.  "mla": q/k = [nope | RoPE] per head, keys and values up-projected from the kv latent (wkv_b);
+    # "latent_mqa" (DeepSeek-V4 family): every head's q lives in the kv_lora_rank-dim latent space, the one shared
+    # KV head is the normalised latent itself (its last qk_rope_head_dim dims carry RoPE), the value is the same
+    # row, and the output's RoPE dims are rotated back by the query position
+    # (king_v10/bundle_v9/cuda_prefill_attn.py:5124-5195: q [s,64,512], kv [s,1,512], d_qk = d_v = 512, rope 64)
+    attn_kind: str = "mla"
+    # grouped low-rank output projection: heads in o_groups groups, each group's concatenated head outputs projected
+    # to o_lora_rank (wo_a, a grouped matmul), then wo_b maps the o_groups*o_lora_rank concatenation to hidden
+    # (reference: wo_a grouped einsum "bhr,hdr->bhd" with 8 groups, wo_b 8192 -> hidden; prefill_gemm.py:15-21).
+    # 0: one dense wo.
+    o_groups: int = 0
+    o_lora_rank: int = 0
+    # sliding window: every query also attends to the last swa_window positions (itself included); with an indexer
+    # the top-k selection is taken over the keys older than the window, so the two sets are disjoint
+    # (reference: SWA window 128, per-row index width 512 top-k + 128 window; rehome_attn.py:8,17-19).  0: off.
+    swa_window: int = 0
     # MoE
     n_routed_experts: int = 256
     n_activated_experts: int = 8
@@ -66,7 +82,22 @@ class ModelConfig:
     # ---- derived -------------------------------------------------------------------------------------------------
     @property
     def qk_head_dim(self) -> int:
+        """Per-head q (and k) width."""
+        if self.attn_kind == "latent_mqa":
+            return self.kv_lora_rank
         return self.qk_nope_head_dim + self.qk_rope_head_dim
+
+    @property
+    def latent_dim(self) -> int:
+        """Width of one cached token row: MLA keeps [kv_lora | RoPE key]; latent MQA keeps the kv_lora_rank row."""
+        if self.attn_kind == "latent_mqa":
+            return self.kv_lora_rank
+        return self.kv_lora_rank + self.qk_rope_head_dim
+
+    @property
+    def head_out_dim(self) -> int:
+        """Per-head attention output width (the input of the output projection per head)."""
+        return self.kv_lora_rank if self.attn_kind == "latent_mqa" else self.v_head_dim
 
     @property
     def hc_mix_dim(self) -> int:
@@ -126,6 +157,12 @@ class ModelConfig:
         assert self.score_func in ("sigmoid", "sqrtsoftplus", "softmax")
         if self.use_indexer:
             assert self.index_head_dim >= self.qk_rope_head_dim
+        assert self.attn_kind in ("mla", "latent_mqa")
+        if self.attn_kind == "latent_mqa":
+            assert 0 < self.qk_rope_head_dim < self.kv_lora_rank
+        if self.o_groups:
+            assert self.n_heads % self.o_groups == 0 and self.o_lora_rank > 0
+        assert self.swa_window >= 0
 
 
 def tiny_config() -> ModelConfig:
@@ -157,7 +194,30 @@ def small_gpu_config() -> ModelConfig:
     )
 
 
-PRESETS = {"tiny": tiny_config, "deepseek_v3": deepseek_v3_config, "small": small_gpu_config}
+def tiny_v4_config() -> ModelConfig:
+    """The tiny CPU model in the DeepSeek-V4 attention layout: latent MQA (one 64-dim latent head with 16 RoPE dims),
+    grouped low-rank output projection, sliding window 16, per-head sinks, DSA index sources, sqrt-softplus router."""
+    return tiny_config().replace(attn_kind="latent_mqa", o_groups=2, o_lora_rank=64, swa_window=16, attn_sink=True,
+                                 index_sources=(0,), index_topk=16, score_func="sqrtsoftplus")
+
+
+def deepseek_v4_config() -> ModelConfig:
+    """DeepSeek-V4.1-Flash-shaped model (the reference's target): 40 layers, hidden 5120, 64 heads of
+    latent MQA over a 512-dim latent (64 RoPE dims), q_lora 1280, 8 output groups with o_lora 1024, window 128,
+    indexer 32 heads x 128 top-512 on source layers 2, 8, 14, 384 experts top-6 (intermediate 2304, sqrt-softplus
+    router), mHC 4 streams.  Layer shapes only: the compressed KV pool, Engram and MXFP4 experts are not modelled."""
+    return ModelConfig(
+        vocab_size=129280, hidden_size=5120, n_layers=40, n_dense_layers=0, dense_intermediate=12288,
+        n_heads=64, q_lora_rank=1280, kv_lora_rank=512, qk_nope_head_dim=448, qk_rope_head_dim=64, v_head_dim=512,
+        max_position=65536, index_n_heads=32, index_head_dim=128, index_topk=512, index_sources=(2, 8, 14),
+        attn_sink=True, attn_kind="latent_mqa", o_groups=8, o_lora_rank=1024, swa_window=128,
+        n_routed_experts=384, n_activated_experts=6, n_shared_experts=1, moe_intermediate=2304,
+        score_func="sqrtsoftplus", route_scale=2.5,
+    )
+
+
+PRESETS = {"tiny": tiny_config, "tiny_v4": tiny_v4_config, "deepseek_v3": deepseek_v3_config,
+           "small": small_gpu_config, "deepseek_v4": deepseek_v4_config}
 
 
 @dataclass

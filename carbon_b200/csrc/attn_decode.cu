@@ -20,6 +20,8 @@ namespace cb {
 namespace mla {
 
 constexpr int HM = 128;                // head rows per CTA (M)
+// A row is NA 64-dim atoms: NA = 9 for MLA (512 latent + 64 RoPE key), NA = 8 for latent MQA (one 512-dim head whose
+// last 64 dims carry RoPE).  The value is always the first DL = 512 dims of the row.
 constexpr int D = 576, DL = 512, DHALF = 256;
 constexpr int KT = 16;                 // keys per tile (N of Q·Kᵀ, K of P·V)
 constexpr int STAGES = 3;
@@ -29,6 +31,8 @@ constexpr int Q_BYTES = 9 * Q_ATOM;    // 144 KB
 constexpr int KV_BYTES = 9 * KV_ATOM;  // 18 KB per stage
 constexpr int P_BYTES = HM * 128;      // 16 KB (16 keys used of a 64-key swizzle atom)
 constexpr int SMEM = 1024 + Q_BYTES + STAGES * KV_BYTES + P_BYTES + 256;
+template <int NA>
+constexpr int smem_bytes() { return 1024 + NA * Q_ATOM + STAGES * NA * KV_ATOM + P_BYTES + 256; }
 constexpr float kRescaleThresh = 8.0f;
 
 struct Params {
@@ -59,10 +63,12 @@ CB_DEVICE void tma_gather4(void* dst, const void* tmap, uint64_t* bar, int col, 
       : "memory");
 }
 
+template <int NA>
 __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constant__ CUtensorMap tm_q,
                                                             const __grid_constant__ CUtensorMap tm_kv,
                                                             const Params p) {
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 1000
+  constexpr int Q_BYTES = NA * Q_ATOM, KV_BYTES = NA * KV_ATOM, D = 64 * NA;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
@@ -106,7 +112,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
     if (lane == 0 && n_tiles > 0) {
       tma_prefetch_desc(&tm_q); tma_prefetch_desc(&tm_kv);
       mbar_arrive_expect_tx(q_full, Q_BYTES);
-      for (int a = 0; a < 9; ++a) tma_load_3d(sQ + a * Q_ATOM, &tm_q, q_full, a * 64, 0, t);
+      for (int a = 0; a < NA; ++a) tma_load_3d(sQ + a * Q_ATOM, &tm_q, q_full, a * 64, 0, t);
     }
     for (int j = 0; j < n_tiles; ++j) {
       const int s = j % STAGES;
@@ -124,7 +130,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
       int r[KT];
 #pragma unroll
       for (int i = 0; i < KT; ++i) r[i] = __shfl_sync(0xffffffffu, slot, i);
-      if (lane < 9) {                                          // lane a issues the 4 gathers of 64-dim atom a
+      if (lane < NA) {                                         // lane a issues the 4 gathers of 64-dim atom a
         uint8_t* dst = sKV + s * KV_BYTES + lane * KV_ATOM;
 #pragma unroll
         for (int g = 0; g < 4; ++g)
@@ -327,20 +333,21 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 }  // namespace mla
 
-// q [T,H,576], kv [S,576] bf16; idx [T,K]; out [T,H,512] bf16. part_o/part_ml: workspace for n_splits > 1
+// q [T,H,D], kv [S,D] bf16 with D = 576 (MLA) or 512 (latent MQA); idx [T,K]; out [T,H,512] bf16.
+// part_o/part_ml: workspace for n_splits > 1
 // (sizes T*n_splits*H*512 and T*n_splits*H*2 floats).
 cudaError_t sparse_mla(const void* q, int T, int H, const void* kv, int S, const int* idx, int K, float scale,
                        int n_splits, float* part_o, float* part_ml, void* out, int* status, cudaStream_t s,
-                       const float* sink) {
+                       const float* sink, int D) {
   using namespace mla;
   if (T == 0) return cudaSuccess;
-  if (H > HM || n_splits < 1) return cudaErrorInvalidValue;
+  if (H > HM || n_splits < 1 || (D != 576 && D != 512)) return cudaErrorInvalidValue;
   auto fn = encode_fn();
   if (!fn) return cudaErrorInvalidValue;
   CUtensorMap tq, tkv;
   {
-    cuuint64_t dims[3] = {D, cuuint64_t(H), cuuint64_t(T)};
-    cuuint64_t str[2] = {D * 2, cuuint64_t(H) * D * 2};
+    cuuint64_t dims[3] = {cuuint64_t(D), cuuint64_t(H), cuuint64_t(T)};
+    cuuint64_t str[2] = {cuuint64_t(D) * 2, cuuint64_t(H) * D * 2};
     cuuint32_t box[3] = {64, HM, 1};
     cuuint32_t es[3] = {1, 1, 1};
     if (fn(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, str, box, es,
@@ -349,8 +356,8 @@ cudaError_t sparse_mla(const void* q, int T, int H, const void* kv, int S, const
       return cudaErrorInvalidValue;
   }
   {
-    cuuint64_t dims[2] = {D, cuuint64_t(S)};
-    cuuint64_t str[1] = {D * 2};
+    cuuint64_t dims[2] = {cuuint64_t(D), cuuint64_t(S)};
+    cuuint64_t str[1] = {cuuint64_t(D) * 2};
     cuuint32_t box[2] = {64, 1};
     cuuint32_t es[2] = {1, 1};
     if (fn(&tkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(kv), dims, str, box, es,
@@ -360,7 +367,10 @@ cudaError_t sparse_mla(const void* q, int T, int H, const void* kv, int S, const
   }
   static bool attr = false;
   if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(sparse_mla_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    cudaError_t e = cudaFuncSetAttribute(sparse_mla_kernel<9>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         smem_bytes<9>());
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(sparse_mla_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes<8>());
     if (e != cudaSuccess) return e;
     attr = true;
   }
@@ -372,7 +382,10 @@ cudaError_t sparse_mla(const void* q, int T, int H, const void* kv, int S, const
   p.out = reinterpret_cast<__nv_bfloat16*>(out);
   p.status = status;
   p.sink = sink;
-  sparse_mla_kernel<<<dim3(T, 2, n_splits), 256, SMEM, s>>>(tq, tkv, p);
+  if (D == 576)
+    sparse_mla_kernel<9><<<dim3(T, 2, n_splits), 256, smem_bytes<9>(), s>>>(tq, tkv, p);
+  else
+    sparse_mla_kernel<8><<<dim3(T, 2, n_splits), 256, smem_bytes<8>(), s>>>(tq, tkv, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || n_splits == 1) return e;
   mla_combine_kernel<<<dim3(T, H), 128, 0, s>>>(part_o, part_ml, n_splits, H, reinterpret_cast<__nv_bfloat16*>(out),

@@ -299,7 +299,8 @@ void topk_mask(torch::Tensor logits, int64_t Tq, int64_t k, torch::Tensor mask, 
                    mask.size(1), row0, cur_stream()));
 }
 
-// q [T, H, 576], kv [S, 576] bf16, idx [T, K] int32 -> out [T, H, 512] bf16
+// q [T, H, D], kv [S, D] bf16 (D = 576 MLA latent + RoPE key, or 512 latent MQA), idx [T, K] int32
+// -> out [T, H, 512] bf16
 void sparse_mla(torch::Tensor q, torch::Tensor kv, torch::Tensor idx, double scale, int64_t n_splits,
                 c10::optional<torch::Tensor> work, torch::Tensor out, c10::optional<torch::Tensor> sink) {
   if (sink.has_value() && sink->defined()) {
@@ -307,7 +308,7 @@ void sparse_mla(torch::Tensor q, torch::Tensor kv, torch::Tensor idx, double sca
   }
   CHECK_CUDA(q); CHECK_DT(q, at::kBFloat16); CHECK_DT(kv, at::kBFloat16); CHECK_DT(idx, at::kInt);
   CHECK_CONTIG(q); CHECK_CONTIG(kv); CHECK_CONTIG(idx); CHECK_CONTIG(out);
-  TORCH_CHECK(q.size(2) == 576 && kv.size(1) == 576 && out.size(2) == 512);
+  TORCH_CHECK((q.size(2) == 576 || q.size(2) == 512) && kv.size(1) == q.size(2) && out.size(2) == 512);
   const int T = q.size(0), H = q.size(1);
   float* po = nullptr;
   float* pml = nullptr;
@@ -318,7 +319,8 @@ void sparse_mla(torch::Tensor q, torch::Tensor kv, torch::Tensor idx, double sca
   }
   c10::cuda::CUDAGuard g(q.device());
   CK(cb::sparse_mla(q.data_ptr(), T, H, kv.data_ptr(), kv.size(0), idx.data_ptr<int>(), idx.size(1), float(scale),
-                    n_splits, po, pml, out.data_ptr(), nullptr, cur_stream(), ptr_or_null<const float>(sink)));
+                    n_splits, po, pml, out.data_ptr(), nullptr, cur_stream(), ptr_or_null<const float>(sink),
+                    int(q.size(2))));
 }
 
 // decode-side DSA: q [T, H, 128] bf16, w [T, H] fp32, kc [S, 128] bf16, key_slots [T, L], n_keys [T] -> out [T, k]

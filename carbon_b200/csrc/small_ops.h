@@ -75,9 +75,10 @@ cudaError_t topk_index(const float* logits, const int* key_slots, const int* n_k
                        int* out, cudaStream_t s);
 
 // tcgen05 absorbed-MLA sparse attention over the latent cache (attn_decode.cu)
-// sink (optional, [H] fp32): per-head attention-sink logit
+// sink (optional, [H] fp32): per-head attention-sink logit; D: row width, 576 (MLA: 512 latent + 64 RoPE key) or
+// 512 (latent MQA: the RoPE dims are the last 64 of the 512); the value is the first 512 dims either way
 cudaError_t sparse_mla(const void* q, int T, int H, const void* kv, int S, const int* idx, int K, float scale,
                        int n_splits, float* part_o, float* part_ml, void* out, int* status, cudaStream_t s,
-                       const float* sink = nullptr);
+                       const float* sink = nullptr, int D = 576);
 
 }  // namespace cb

@@ -1,7 +1,7 @@
 """Paged latent KV cache.
 
-Per layer the cache holds, for every token slot, the MLA latent row ``[kv_lora | rope]`` (the only per-token state
-absorbed MLA needs; one row serves all heads) and, when the model has a DSA indexer, the indexer key row.  Slots are
+Per layer the cache holds, for every token slot, the latent row: ``[kv_lora | RoPE key]`` for MLA (the only
+per-token state absorbed MLA needs; one row serves all heads) or the kv_lora_rank row itself for latent MQA and, when the model has a DSA indexer, the indexer key row.  Slots are
 grouped into pages of ``page_size`` tokens; a request owns a list of pages (its page table) and token ``p`` of the
 request lives in slot ``pages[p // page_size] * page_size + p % page_size``.
 
@@ -25,7 +25,7 @@ class PagedLatentCache:
         self.page_size = page_size
         self.num_pages = num_pages
         self.num_slots = num_pages * page_size
-        width = cfg.kv_lora_rank + cfg.qk_rope_head_dim
+        width = cfg.latent_dim
         self.latent: List[torch.Tensor] = [torch.zeros(self.num_slots, width, dtype=dtype, device=device)
                                            for _ in range(n_layers)]
         # indexer keys only for layers that run the indexer (index-source layers share their selection)
@@ -47,4 +47,4 @@ class PagedLatentCache:
     @staticmethod
     def bytes_per_token(cfg: ModelConfig, n_layers: int, elem: int = 2) -> int:
         n_idx = sum(1 for l in range(n_layers) if cfg.has_indexer(l))
-        return (cfg.kv_lora_rank + cfg.qk_rope_head_dim) * elem * n_layers + cfg.index_head_dim * elem * n_idx
+        return cfg.latent_dim * elem * n_layers + cfg.index_head_dim * elem * n_idx

@@ -153,6 +153,8 @@ class DeepseekModel:
         self._side = None          # side stream of the shared expert
         self._dsa = {}
         cfg.validate()
+        if cfg.swa_window and cfg.attn_kind != "latent_mqa":
+            raise NotImplementedError("swa_window is served by the latent-MQA attention path only")
         tp, ep = self.pctx.tp, self.pctx.ep
         self.H_local = cfg.n_heads // tp
         self.E_local = cfg.n_routed_experts // ep if cfg.n_routed_experts else 0
@@ -190,24 +192,39 @@ class DeepseekModel:
         L.ffn_norm = get(p + "ffn_norm.weight")
         H, Hl, dn, dr, dv, r = cfg.n_heads, self.H_local, cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, \
             cfg.v_head_dim, cfg.kv_lora_rank
+        dq, dvh = cfg.qk_head_dim, cfg.head_out_dim
         h0, h1 = pc.tp_rank * Hl, (pc.tp_rank + 1) * Hl
         a = p + "attn."
         if cfg.q_lora_rank > 0:
             L.wq_a = Lin(get(a + "wq_a.weight"), dev, self.fp8)
             L.q_norm = get(a + "q_norm.weight")
-            L.wq_b = Lin(get(a + "wq_b.weight", slice(h0 * (dn + dr), h1 * (dn + dr))), dev, self.fp8)
+            L.wq_b = Lin(get(a + "wq_b.weight", slice(h0 * dq, h1 * dq)), dev, self.fp8)
         else:
-            L.wq = Lin(get(a + "wq.weight", slice(h0 * (dn + dr), h1 * (dn + dr))), dev, self.fp8)
+            L.wq = Lin(get(a + "wq.weight", slice(h0 * dq, h1 * dq)), dev, self.fp8)
         L.wkv_a = Lin(get(a + "wkv_a.weight"), dev, self.fp8)
         L.kv_norm = get(a + "kv_norm.weight")
-        wkv_b = get(a + "wkv_b.weight", slice(h0 * (dn + dv), h1 * (dn + dv)))      # [Hl*(dn+dv), r]
-        L.wkv_b = Lin(wkv_b, dev, self.fp8)
-        # absorbed decode uses the same (fp8-rounded) wkv_b as the prefill GEMM
-        wkv_b3 = (L.wkv_b.fw.dequant() if L.wkv_b.kind == "fp8" else wkv_b).view(Hl, dn + dv, r)
-        L.w_uk = wkv_b3[:, :dn, :].transpose(1, 2).contiguous().to(self.act_dtype)  # [Hl, r, dn]: q_abs = q_nope·w_ukᵀ
-        L.w_uv = wkv_b3[:, dn:, :].contiguous().to(self.act_dtype)                  # [Hl, dv, r]
-        wo = get(a + "wo.weight")                                                  # [D, H*dv]
-        L.wo = Lin(wo[:, h0 * dv:h1 * dv].contiguous(), dev, self.fp8)
+        L.wkv_b = None
+        if cfg.attn_kind == "mla":
+            wkv_b = get(a + "wkv_b.weight", slice(h0 * (dn + dv), h1 * (dn + dv)))  # [Hl*(dn+dv), r]
+            L.wkv_b = Lin(wkv_b, dev, self.fp8)
+            # absorbed decode uses the same (fp8-rounded) wkv_b as the prefill GEMM
+            wkv_b3 = (L.wkv_b.fw.dequant() if L.wkv_b.kind == "fp8" else wkv_b).view(Hl, dn + dv, r)
+            L.w_uk = wkv_b3[:, :dn, :].transpose(1, 2).contiguous().to(self.act_dtype)  # [Hl, r, dn]
+            L.w_uv = wkv_b3[:, dn:, :].contiguous().to(self.act_dtype)                  # [Hl, dv, r]
+        L.wo_a = None
+        if cfg.o_groups:
+            # grouped low-rank output projection: this rank's heads are whole groups
+            G, R = cfg.o_groups, cfg.o_lora_rank
+            if G % pc.tp:
+                raise ValueError(f"o_groups={G} must be a multiple of the attention TP degree {pc.tp}")
+            Gl = G // pc.tp
+            g0 = pc.tp_rank * Gl
+            L.wo_a = get(a + "wo_a.weight", slice(g0, g0 + Gl)).to(self.act_dtype).contiguous()  # [Gl, R, (H/G)*dvh]
+            wo_b = get(a + "wo_b.weight")                                                      # [D, G*R]
+            L.wo = Lin(wo_b[:, g0 * R:(g0 + Gl) * R].contiguous(), dev, self.fp8)
+        else:
+            wo = get(a + "wo.weight")                                              # [D, H*dvh]
+            L.wo = Lin(wo[:, h0 * dvh:h1 * dvh].contiguous(), dev, self.fp8)
         L.sink = get(a + "sink")[h0:h1].float().contiguous() if cfg.attn_sink else None
         L.sink_all = get(a + "sink").float().contiguous().to(dev) if cfg.attn_sink else None     # every head
         L.has_indexer = cfg.has_indexer(i)
@@ -309,12 +326,19 @@ class DeepseekModel:
             else:
                 q_lat_l = h
         with region("attn.kv_proj"):
-            kv = L.wkv_a(h, xq=hq)                                                  # [T_l, r + dr]
-            kv_c = C.rms_norm(kv[:, :r].contiguous(), L.kv_norm, cfg.rms_eps) if self.on_gpu else \
-                R.rms_norm(kv[:, :r], L.kv_norm, cfg.rms_eps)
-            k_pe = kv[:, r:].contiguous().view(-1, 1, dr)
-            C.rope_(k_pe, 0, dr, self.cos_sin, pos_l)
-            latent_l = torch.cat([kv_c.to(self.act_dtype), k_pe.view(-1, dr).to(self.act_dtype)], dim=-1)
+            kv = L.wkv_a(h, xq=hq)                                                  # [T_l, latent_dim]
+            if cfg.attn_kind == "latent_mqa":
+                # the shared KV head: the normalised latent with RoPE on its last dr dims
+                kv_c = C.rms_norm(kv.contiguous(), L.kv_norm, cfg.rms_eps) if self.on_gpu else \
+                    R.rms_norm(kv, L.kv_norm, cfg.rms_eps)
+                latent_l = kv_c.to(self.act_dtype).contiguous()
+                C.rope_(latent_l.view(-1, 1, r), r - dr, dr, self.cos_sin, pos_l)
+            else:
+                kv_c = C.rms_norm(kv[:, :r].contiguous(), L.kv_norm, cfg.rms_eps) if self.on_gpu else \
+                    R.rms_norm(kv[:, :r], L.kv_norm, cfg.rms_eps)
+                k_pe = kv[:, r:].contiguous().view(-1, 1, dr)
+                C.rope_(k_pe, 0, dr, self.cos_sin, pos_l)
+                latent_l = torch.cat([kv_c.to(self.act_dtype), k_pe.view(-1, dr).to(self.act_dtype)], dim=-1)
         idx_l = None
         if L.has_indexer:
             with region("attn.indexer_qk"):
@@ -335,21 +359,33 @@ class DeepseekModel:
             if idx_k is not None:
                 cache.write_index_k(i, out_loc, idx_k)
         T = q_lat.shape[0]
+        dq = cfg.qk_head_dim
         with region("attn.q_proj"):
             if cfg.q_lora_rank > 0:
-                q = L.wq_b(q_lat).view(T, Hl, dn + dr)
+                q = L.wq_b(q_lat).view(T, Hl, dq)
             else:
-                q = L.wq(q_lat).view(T, Hl, dn + dr)
+                q = L.wq(q_lat).view(T, Hl, dq)
             if not self.on_gpu:
                 q = q.clone()
-            C.rope_(q, dn, dr, self.cos_sin, pos_l if dp else fb.pos)
-        if fb.is_prefill:
+            C.rope_(q, dq - dr, dr, self.cos_sin, pos_l if dp else fb.pos)
+        if cfg.attn_kind == "latent_mqa":
+            o = self._attn_latent(i, q, fb, cache, idx_l, dp)
+        elif fb.is_prefill:
             o = self._attn_prefill(i, q, latent, fb, idx_l, cache, dp)
         else:
             o = self._attn_decode(i, q, fb, cache, idx_l, dp)
         with region("attn.o_proj"):
-            o2 = o.reshape(T, Hl * dv).to(self.act_dtype).contiguous()
+            o2 = self._out_heads(L, o, T)
             return L.wo(o2) if dp else pc.row_parallel_out(L.wo, o2)
+
+    def _out_heads(self, L, o: torch.Tensor, T: int) -> torch.Tensor:
+        """Per-head outputs [T, Hl, dvh] -> the output projection's input: the head concatenation, or (grouped
+        low-rank projection) wo_a of each local group of heads, [T, Gl * o_lora]."""
+        if L.wo_a is None:
+            return o.reshape(T, -1).to(self.act_dtype).contiguous()
+        Gl = L.wo_a.shape[0]
+        z = head_bmm(o.reshape(T, Gl, -1).to(self.act_dtype), L.wo_a)                # [T, Gl, o_lora]
+        return z.reshape(T, -1).to(self.act_dtype).contiguous()
 
     def indexer_qkw(self, i, h, q_lat, pos):
         cfg, L = self.cfg, self.layers[i]
@@ -399,6 +435,87 @@ class DeepseekModel:
             masks = self._dsa.get(src)              # selection shared with the index-source layer
         with region("attn.core_prefill"):
             return A.mla_prefill(q, kvb, latent[:, r:].contiguous(), cu, cfg.softmax_scale, masks, sink=L.sink)
+
+    def _latent_keys(self, i, fb, cache, idx_l, rows, local: bool) -> torch.Tensor:
+        """Cache slots each query in ``rows`` (a slice of the batch) attends to, [Tq, K] int32 (-1 pad): the last
+        swa_window positions, plus the DSA top-k over the older keys (or every causal key without an indexer)."""
+        cfg, pc = self.cfg, self.pctx
+        W, lo, hi = cfg.swa_window, pc.local[0], pc.local[1]
+        dev = fb.pos.device
+        if fb.is_prefill:
+            # keys of a prefill query: its own sequence's slots, positions 0..p (prompts start at position 0)
+            cu = fb.cu_seqlens
+            lens = [b - a for a, b in zip(cu[:-1], cu[1:])]
+            start = torch.repeat_interleave(torch.tensor(cu[:-1], dtype=torch.long),
+                                            torch.tensor(lens, dtype=torch.long)).to(dev)[rows]
+            nk = fb.pos[rows].long() + 1
+            Lmax = max(lens) if lens else 1
+            j = torch.arange(Lmax, device=dev)
+            src_i = (start[:, None] + j[None, :]).clamp(max=fb.out_loc.shape[0] - 1)
+            ks = torch.where(j[None, :] < nk[:, None], fb.out_loc[src_i].long(), -1).to(torch.int32)
+        else:
+            ks, nk = fb.key_slots[rows], fb.n_keys[rows].long()
+        parts = []
+        src = cfg.index_source(i)
+        if src is not None:
+            if src == i:
+                with region("attn.indexer_topk"):
+                    qi, _, wi = idx_l
+                    if fb.is_prefill:
+                        ks_l = ks if local else self._latent_key_table(fb, lo, hi)
+                        nk_l = (fb.pos[lo:hi].long() + 1) if not local else nk
+                    else:
+                        ks_l, nk_l = fb.key_slots[lo:hi], fb.n_keys[lo:hi].long()
+                    cand = (nk_l - W).clamp(min=0).to(torch.int32).contiguous()      # keys older than the window
+                    sel = A.indexer_topk(qi, wi, cache.index_k[i], ks_l.contiguous(), cand, cfg.index_topk)
+                    sel = sel if local else pc.gather_rows(sel)
+                self._dsa[i] = sel
+            else:
+                sel = self._dsa[src]                # selection shared with the index-source layer
+            parts.append(sel)
+        if W > 0:
+            wj = nk[:, None] - W + torch.arange(W, device=dev)[None, :]
+            win = torch.where(wj >= 0, ks.gather(1, wj.clamp(min=0)).long(), -1).to(torch.int32)
+            parts.append(win)
+        elif src is None:
+            parts.append(ks)                        # dense causal
+        return torch.cat([p.to(torch.int32) for p in parts], dim=1).contiguous()
+
+    def _latent_key_table(self, fb, lo, hi) -> torch.Tensor:
+        """Prefill key slots [hi-lo, Lmax] of this rank's queries (the indexer's candidate table)."""
+        cu = fb.cu_seqlens
+        lens = [b - a for a, b in zip(cu[:-1], cu[1:])]
+        dev = fb.pos.device
+        start = torch.repeat_interleave(torch.tensor(cu[:-1], dtype=torch.long),
+                                        torch.tensor(lens, dtype=torch.long)).to(dev)[lo:hi]
+        nk = fb.pos[lo:hi].long() + 1
+        j = torch.arange(max(lens) if lens else 1, device=dev)
+        src_i = (start[:, None] + j[None, :]).clamp(max=fb.out_loc.shape[0] - 1)
+        return torch.where(j[None, :] < nk[:, None], fb.out_loc[src_i].long(), -1).to(torch.int32)
+
+    def _attn_latent(self, i, q, fb, cache, idx_l, dp: bool = False):
+        """Latent MQA (DeepSeek-V4 layout), prefill and decode alike: every head attends over explicit per-query key
+        lists of cached latent rows (sparse kernel), then the output's RoPE dims are rotated back by the query
+        position.  Tensor-parallel heads run token-parallel through a head/token all-to-all, so every rank reads
+        only its own queries' key rows."""
+        cfg, L, pc = self.cfg, self.layers[i], self.pctx
+        r, dr = cfg.kv_lora_rank, cfg.qk_rope_head_dim
+        lo, hi = pc.local
+        swap = not dp and pc.world > 1 and hasattr(pc, "heads_to_tokens")
+        local = dp or swap
+        rows = slice(lo, hi) if local else slice(0, q.shape[0])
+        idx = self._latent_keys(i, fb, cache, idx_l, rows, local)
+        pos_q = fb.pos[lo:hi] if dp else fb.pos
+        with region("attn.core_prefill" if fb.is_prefill else "attn.core_decode"):
+            if swap:
+                q_tok = pc.heads_to_tokens(q.contiguous())                          # [n_r, H, r]
+                o_tok = A.sparse_mla(q_tok, cache.latent[i], idx, cfg.softmax_scale, r, sink=L.sink_all)
+                o = pc.tokens_to_heads(o_tok.contiguous()) if self.on_gpu else pc.tokens_to_heads(o_tok)
+            else:
+                o = A.sparse_mla(q.contiguous(), cache.latent[i], idx, cfg.softmax_scale, r, sink=L.sink)
+            o = o.to(self.act_dtype).contiguous() if self.on_gpu else o.float().contiguous()
+            C.rope_(o, r - dr, dr, self.cos_sin, pos_q, inverse=True)
+        return o
 
     def _attn_decode(self, i, q, fb, cache, idx_l, dp: bool = False):
         cfg, L, pc = self.cfg, self.layers[i], self.pctx

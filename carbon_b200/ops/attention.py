@@ -151,14 +151,15 @@ def sparse_mla(q: torch.Tensor, kv: torch.Tensor, idx: torch.Tensor, scale: floa
     T, H, D = q.shape
     if q.is_cuda:
         e = ext()
-        if hasattr(e, "sparse_mla") and D == 576 and d_latent == 512 and H <= 128:
+        if hasattr(e, "sparse_mla") and D in (576, 512) and d_latent == 512 and H <= 128:
             out = torch.empty(T, H, d_latent, dtype=torch.bfloat16, device=q.device)
             splits = mla_splits(T, idx.shape[1], q.device)
             work = torch.empty(T * splits * H * 514, dtype=torch.float32, device=q.device) if splits > 1 else None
             e.sparse_mla(q, kv, idx, float(scale), splits, work, out,
                          sink.float().contiguous() if sink is not None else None)
             return out
-        raise RuntimeError("sparse_mla: the tcgen05 kernel needs D=576 (512 latent + 64 RoPE), d_latent=512, H<=128")
+        raise RuntimeError("sparse_mla: the tcgen05 kernel needs D=576 (512 latent + 64 RoPE key) or D=512 (latent "
+                           "MQA), d_latent=512, H<=128")
     out = torch.zeros(T, H, d_latent)
     for t in range(T):
         sel = idx[t][idx[t] >= 0].long()

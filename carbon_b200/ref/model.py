@@ -45,10 +45,16 @@ def param_shapes(cfg: ModelConfig) -> "OrderedDict[str, Tuple[Tuple[int, ...], s
             p[L + "attn.wq_b.weight"] = ((H * cfg.qk_head_dim, cfg.q_lora_rank), "normal")
         else:
             p[L + "attn.wq.weight"] = ((H * cfg.qk_head_dim, D), "normal")
-        p[L + "attn.wkv_a.weight"] = ((cfg.kv_lora_rank + cfg.qk_rope_head_dim, D), "normal")
+        p[L + "attn.wkv_a.weight"] = ((cfg.latent_dim, D), "normal")
         p[L + "attn.kv_norm.weight"] = ((cfg.kv_lora_rank,), "ones")
-        p[L + "attn.wkv_b.weight"] = ((H * (cfg.qk_nope_head_dim + cfg.v_head_dim), cfg.kv_lora_rank), "normal")
-        p[L + "attn.wo.weight"] = ((D, H * cfg.v_head_dim), "normal")
+        if cfg.attn_kind == "mla":
+            p[L + "attn.wkv_b.weight"] = ((H * (cfg.qk_nope_head_dim + cfg.v_head_dim), cfg.kv_lora_rank), "normal")
+        if cfg.o_groups:
+            G = cfg.o_groups
+            p[L + "attn.wo_a.weight"] = ((G, cfg.o_lora_rank, H // G * cfg.head_out_dim), "normal")
+            p[L + "attn.wo_b.weight"] = ((D, G * cfg.o_lora_rank), "normal")
+        else:
+            p[L + "attn.wo.weight"] = ((D, H * cfg.head_out_dim), "normal")
         if cfg.attn_sink:
             p[L + "attn.sink"] = ((H,), "normal")
         if cfg.has_indexer(i):
@@ -117,31 +123,66 @@ class RefModel:
         cfg, w = self.cfg, self.w
         L = f"layers.{i}.attn."
         T, H = h.shape[0], cfg.n_heads
-        dn, dr, dv, r = cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, cfg.v_head_dim, cfg.kv_lora_rank
+        dr, r, dq = cfg.qk_rope_head_dim, cfg.kv_lora_rank, cfg.qk_head_dim
         if cfg.q_lora_rank > 0:
             q_lat = ops.rms_norm(h @ w[L + "wq_a.weight"].t(), w[L + "q_norm.weight"], cfg.rms_eps)
-            q = (q_lat @ w[L + "wq_b.weight"].t()).view(T, H, dn + dr)
+            q = (q_lat @ w[L + "wq_b.weight"].t()).view(T, H, dq)
         else:
             q_lat = h
-            q = (h @ w[L + "wq.weight"].t()).view(T, H, dn + dr)
-        q_nope, q_pe = q[..., :dn], ops.apply_rope(q[..., dn:], pos, cfg.rope_theta)
+            q = (h @ w[L + "wq.weight"].t()).view(T, H, dq)
+        dn = dq - dr                                  # non-RoPE part of q
+        qf = torch.cat([q[..., :dn], ops.apply_rope(q[..., dn:], pos, cfg.rope_theta)], dim=-1)
         kv = h @ w[L + "wkv_a.weight"].t()
-        kv_c = ops.rms_norm(kv[:, :r], w[L + "kv_norm.weight"], cfg.rms_eps)
-        k_pe = ops.apply_rope(kv[:, None, r:], pos, cfg.rope_theta)            # [T,1,dr]
-        kvb = (kv_c @ w[L + "wkv_b.weight"].t()).view(T, H, dn + dv)
-        k = torch.cat([kvb[..., :dn], k_pe.expand(T, H, dr)], dim=-1)
-        v = kvb[..., dn:]
-        qf = torch.cat([q_nope, q_pe], dim=-1)
+        if cfg.attn_kind == "latent_mqa":
+            # one shared head: the normalised latent, RoPE on its last dr dims; value = the same row
+            kv_c = ops.rms_norm(kv, w[L + "kv_norm.weight"], cfg.rms_eps)
+            k = torch.cat([kv_c[:, :r - dr], ops.apply_rope(kv_c[:, None, r - dr:], pos, cfg.rope_theta)[:, 0]],
+                          dim=-1)[:, None, :]                                   # [T,1,r]
+            v = k
+        else:
+            dv = cfg.v_head_dim
+            kv_c = ops.rms_norm(kv[:, :r], w[L + "kv_norm.weight"], cfg.rms_eps)
+            k_pe = ops.apply_rope(kv[:, None, r:], pos, cfg.rope_theta)         # [T,1,dr]
+            kvb = (kv_c @ w[L + "wkv_b.weight"].t()).view(T, H, dn + dv)
+            k = torch.cat([kvb[..., :dn], k_pe.expand(T, H, dr)], dim=-1)
+            v = kvb[..., dn:]
+        W = cfg.swa_window
+        window = None
+        if W > 0:
+            window = (pos[None, :] > pos[:, None] - W) & (pos[None, :] <= pos[:, None])
         allowed = None
         src = cfg.index_source(i)
         if src == i:
-            allowed = ops.topk_mask(self.indexer_logits(i, h, q_lat, pos), pos, pos, cfg.index_topk)
+            logits = self.indexer_logits(i, h, q_lat, pos)
+            if window is not None:                      # top-k over the keys older than the window
+                logits = logits.masked_fill(window, float("-inf"))
+            allowed = ops.topk_mask(logits, pos, pos, cfg.index_topk)
+            if window is not None:
+                allowed = allowed & ~window
             self._dsa[i] = allowed
         elif src is not None:
             allowed = self._dsa[src]           # shared selection of the source layer
+        if window is not None:
+            allowed = window if allowed is None else (allowed | window)
         sink = w[L + "sink"] if cfg.attn_sink else None
-        o = ops.causal_attention(qf, k, v, cfg.softmax_scale, pos, pos, allowed, sink=sink)
-        return o.reshape(T, H * dv) @ w[L + "wo.weight"].t()
+        o = ops.causal_attention(qf, k, v, cfg.softmax_scale, pos, pos, allowed, sink=sink)   # [T,H,dvh]
+        if cfg.attn_kind == "latent_mqa":
+            # the value's RoPE dims carry each key's rotation: rotate the output back by the query position
+            o = torch.cat([o[..., :r - dr], ops.apply_rope(o[..., r - dr:], pos, cfg.rope_theta, inverse=True)],
+                          dim=-1)
+        return self.out_proj(i, o)
+
+    def out_proj(self, i: int, o: torch.Tensor) -> torch.Tensor:
+        """o [T, H, dvh] -> [T, D]: one dense wo, or the grouped low-rank wo_a (per group of heads) then wo_b."""
+        cfg, w = self.cfg, self.w
+        L = f"layers.{i}.attn."
+        T, H = o.shape[0], o.shape[1]
+        if not cfg.o_groups:
+            return o.reshape(T, -1) @ w[L + "wo.weight"].t()
+        G = cfg.o_groups
+        og = o.reshape(T, G, -1)                                                # [T, G, (H/G)*dvh]
+        z = torch.einsum("tgk,gnk->tgn", og, w[L + "wo_a.weight"])              # [T, G, o_lora]
+        return z.reshape(T, -1) @ w[L + "wo_b.weight"].t()
 
     def indexer_logits(self, i: int, h: torch.Tensor, q_lat: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
         q, k, wt = self.indexer_qkw(i, h, q_lat, pos)

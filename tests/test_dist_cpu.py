@@ -28,7 +28,13 @@ def _prompts(cfg):
     return [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (64, 50, 70)]
 
 
-def _worker(rank, world, port, q, attn_dp=False):
+def _cfg(variant):
+    from carbon_b200.config import tiny_v4_config
+
+    return tiny_v4_config().replace(n_layers=3, index_sources=(1,)) if variant == "v4" else tiny_config()
+
+
+def _worker(rank, world, port, q, attn_dp=False, variant="v3"):
     from datetime import timedelta
 
     from carbon_b200.parallel.dist import DistCtx
@@ -37,7 +43,7 @@ def _worker(rank, world, port, q, attn_dp=False):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
     try:
-        cfg = tiny_config()
+        cfg = _cfg(variant)
         w = init_weights(cfg, seed=0)
         eng = Engine(cfg, device="cpu", source=WeightSource(cfg, state=w), num_pages=32, page_size=16,
                      pctx=DistCtx(rank, world, attn_dp=attn_dp))
@@ -47,16 +53,17 @@ def _worker(rank, world, port, q, attn_dp=False):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,attn_dp", [(2, False), (2, True)])
-def test_tp_ep_engine_matches_single_rank(world, attn_dp):
-    cfg = tiny_config()
+@pytest.mark.parametrize("world,attn_dp,variant", [(2, False, "v3"), (2, True, "v3"), (2, False, "v4"),
+                                                   (2, True, "v4")])
+def test_tp_ep_engine_matches_single_rank(world, attn_dp, variant):
+    cfg = _cfg(variant)
     w = init_weights(cfg, seed=0)
     single = Engine(cfg, device="cpu", source=WeightSource(cfg, state=w), num_pages=32, page_size=16)
     outs_ref, hist_ref = single.generate(_prompts(cfg), max_new_tokens=6, return_logits=True)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q, attn_dp)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, attn_dp, variant)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=300) for _ in range(world)]

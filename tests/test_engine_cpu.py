@@ -2,7 +2,7 @@
 the naive full-recompute fp32 oracle within 1e-4 on every prefill and greedy-decode step."""
 import torch
 
-from carbon_b200.config import tiny_config
+from carbon_b200.config import tiny_config, tiny_v4_config
 from carbon_b200.engine.engine import Engine
 from carbon_b200.models.weights import WeightSource
 from carbon_b200.ref.model import RefModel, init_weights
@@ -11,13 +11,19 @@ from carbon_b200.ref.model import RefModel, init_weights
 import pytest
 
 
-@pytest.mark.parametrize("variant", ["v3", "v41_features"])
+@pytest.mark.parametrize("variant", ["v3", "v41_features", "v4_latent", "v4_latent_nodsa"])
 def test_tiny_engine_matches_oracle(variant):
     """v41_features: DSA selection computed by index-source layers 1 and 3 only (layer 0 dense, layer 2 reuses
-    layer 1's selection) and per-head attention sinks."""
+    layer 1's selection) and per-head attention sinks.  v4_latent: the V4 attention layout (latent MQA with output
+    RoPE rotated back, grouped low-rank output projection, sliding window 16 + top-16 over older keys, sinks,
+    sqrt-softplus router); v4_latent_nodsa: the same without the indexer on layer 0 (window-only attention there)."""
     cfg = tiny_config()
     if variant == "v41_features":
         cfg = cfg.replace(n_layers=4, index_sources=(1, 3), attn_sink=True)
+    elif variant == "v4_latent":
+        cfg = tiny_v4_config().replace(n_layers=3, index_sources=(1,))
+    elif variant == "v4_latent_nodsa":
+        cfg = tiny_v4_config().replace(index_n_heads=0)
     w = init_weights(cfg, seed=0)
     ref = RefModel(cfg, w)
     g = torch.Generator().manual_seed(1)

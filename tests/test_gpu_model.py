@@ -15,7 +15,7 @@ from carbon_b200.ref.model import RefModel, init_weights
 
 pytestmark = pytest.mark.gpu
 
-FP8_NAMES = ("wq_a.weight", "wq_b.weight", "wkv_a.weight", "wkv_b.weight", "wo.weight", "ffn.w1", "ffn.w2",
+FP8_NAMES = ("wq_a.weight", "wq_b.weight", "wkv_a.weight", "wkv_b.weight", "wo.weight", "wo_b.weight", "ffn.w1", "ffn.w2",
              "ffn.w3", "experts.w1", "experts.w2", "experts.w3", "shared.w1", "shared.w2", "shared.w3")
 
 
@@ -113,3 +113,57 @@ def test_smoke_entry():
     from carbon_b200.engine.smoke import run_smoke
 
     run_smoke()
+
+
+def _v4_cfg(n_layers=2):
+    """The V4 attention layout at kernel-compatible sizes: latent MQA over a 512-dim latent (64 RoPE dims), 16 heads
+    in 4 output groups (o_lora 256), window 64 + top-128 over older keys, sinks, sqrt-softplus router."""
+    return small_gpu_config().replace(n_layers=n_layers, n_routed_experts=8, n_activated_experts=2, vocab_size=2048,
+                                      attn_kind="latent_mqa", o_groups=4, o_lora_rank=256, swa_window=64,
+                                      attn_sink=True, index_topk=128, score_func="sqrtsoftplus")
+
+
+@pytest.mark.parametrize("plen", [48, 300])
+def test_v4_latent_mqa_model_vs_oracle(plen):
+    cfg = _v4_cfg()
+    w = fp8_roundtrip(init_weights(cfg, seed=0))
+    ref = RefModel(cfg, w)
+    g = torch.Generator().manual_seed(1)
+    prompt = torch.randint(0, cfg.vocab_size, (plen,), generator=g)
+    eng = Engine(cfg, device="cuda", source=WeightSource(cfg, state=w), num_pages=32, page_size=64)
+    eng.model.trace = []
+    r = eng.add_request(prompt.tolist())
+    got = eng.prefill([r])[0].float().cpu()
+    ref.forced_routing = {int(k.split(".")[0]): v.long() for k, v in eng.model.trace if k.endswith("router_ids")}
+    exp = ref.forward(prompt)[-1]
+    assert _rel(got, exp) < 0.15, _rel(got, exp)
+    assert torch.corrcoef(torch.stack([got, exp]))[0, 1] > 0.98
+
+
+def test_v4_latent_mqa_decode_matches_prefill():
+    cfg = _v4_cfg()
+    src = WeightSource(cfg, seed=7)
+    eng = Engine(cfg, device="cuda", source=src, num_pages=32, page_size=64)
+    g = torch.Generator().manual_seed(3)
+    prompt = torch.randint(0, cfg.vocab_size, (281,), generator=g).tolist()
+    r1 = eng.add_request(prompt[:-1])
+    eng.prefill([r1])
+    dec = eng.decode([r1], [prompt[-1]])[0].float().cpu()
+    r2 = eng.add_request(prompt)
+    full = eng.prefill([r2])[0].float().cpu()
+    assert _rel(dec, full) < 0.1, _rel(dec, full)
+    assert torch.corrcoef(torch.stack([dec, full]))[0, 1] > 0.99
+
+
+def test_v4_latent_mqa_cuda_graph_decode_matches_eager():
+    cfg = _v4_cfg()
+    src = WeightSource(cfg, seed=3)
+    g = torch.Generator().manual_seed(2)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (200, 33, 5)]
+    e1 = Engine(cfg, device="cuda", source=src, num_pages=32, page_size=64, cuda_graphs=False)
+    o1, h1 = e1.generate(prompts, 4, return_logits=True)
+    e2 = Engine(cfg, device="cuda", model=e1.model, num_pages=32, page_size=64, cuda_graphs=True, graph_buckets=(4,))
+    o2, h2 = e2.generate(prompts, 4, return_logits=True)
+    assert o1 == o2
+    for a, b in zip(h1, h2):
+        assert torch.allclose(a, b, atol=1e-3, rtol=1e-3)
