@@ -4,6 +4,11 @@
   [ceil(N/128), ceil(K/128)], the value that multiplies each 128×128 block (DeepSeek-V3's ``weight_scale_inv``).
 * Everything else (norms, router, mHC parameters, embedding, head) is stored in bf16 / fp32 as is.
 * Experts may be stored stacked (``ffn.experts.w1`` [E, I, D]) or per expert (``ffn.experts.{e}.w1``); both load.
+* Routed-expert weights may instead be MXFP4 (the reference's expert format, ``moe_prefill.py:14-16``): ``<name>`` is
+  uint8 [.., N, K/2] (two e2m1 codes per byte, low nibble first) next to ``<name>_scale`` uint8 [.., N, K/32] (UE8M0
+  exponent of each 32-element block).  They load as their exact values; the engine then stores them in its fp8
+  128x128 block format (exact whenever a 128x128 block's 32-element scales span at most 2^7, i.e. almost always;
+  otherwise the smallest values round).
 
 ``save_checkpoint`` writes this format from a state dict (quantising the fp8 names with ``ref.ops.quant_fp8_blocks``,
 so scales are powers of two); ``CheckpointSource`` is a ``WeightSource`` that reads it lazily, dequantising on the
@@ -23,7 +28,8 @@ from ..config import ModelConfig
 from ..ref import ops as R
 from .weights import WeightSource
 
-FP8_SUFFIXES = ("wq_a.weight", "wq_b.weight", "wkv_a.weight", "wkv_b.weight", "wo.weight", "ffn.w1", "ffn.w2",
+FP8_SUFFIXES = ("wq_a.weight", "wq_b.weight", "wkv_a.weight", "wkv_b.weight", "wo.weight", "wo_b.weight", "ffn.w1",
+                "ffn.w2",
                 "ffn.w3", "experts.w1", "experts.w2", "experts.w3", "shared.w1", "shared.w2", "shared.w3")
 _EXPERT_RE = re.compile(r"^(layers\.\d+\.ffn\.experts)\.(\d+)\.(w[123])$")
 
@@ -33,14 +39,24 @@ def is_fp8_name(name: str) -> bool:
 
 
 def save_checkpoint(state: Dict[str, torch.Tensor], path: str, shard_bytes: int = 2 << 30,
-                    per_expert: bool = False) -> None:
-    """Write ``state`` (fp32 tensors) as fp8 block-scaled safetensors shards + an index JSON."""
+                    per_expert: bool = False, mxfp4_experts: bool = False) -> None:
+    """Write ``state`` (fp32 tensors) as fp8 block-scaled safetensors shards + an index JSON (routed experts in MXFP4
+    when ``mxfp4_experts``)."""
     from safetensors.torch import save_file
 
     os.makedirs(path, exist_ok=True)
     out: Dict[str, torch.Tensor] = {}
     for name, t in state.items():
-        if is_fp8_name(name):
+        if mxfp4_experts and name.endswith(("experts.w1", "experts.w2", "experts.w3")):
+            qs = [R.quant_mxfp4(t[e].float()) for e in range(t.shape[0])]
+            if per_expert:
+                for e, (q, s) in enumerate(qs):
+                    n2 = f"{name[:-3]}.{e}.{name[-2:]}"
+                    out[n2], out[n2 + "_scale"] = q, s
+            else:
+                out[name] = torch.stack([q for q, _ in qs])
+                out[name + "_scale"] = torch.stack([s for _, s in qs])
+        elif is_fp8_name(name):
             if t.dim() == 3:
                 mats = [(f"{name[:-3]}.{e}.{name[-2:]}" if per_expert else None, t[e]) for e in range(t.shape[0])]
                 if per_expert:
@@ -126,6 +142,11 @@ class CheckpointSource(WeightSource):
 
     def _load(self, name: str, device) -> torch.Tensor:
         t = self._tensor(name)
+        if t.dtype == torch.uint8 and self.has(name + "_scale"):          # MXFP4
+            s = self._tensor(name + "_scale")
+            if t.dim() == 3:
+                return torch.stack([R.dequant_mxfp4(t[e].to(device), s[e].to(device)) for e in range(t.shape[0])])
+            return R.dequant_mxfp4(t.to(device), s.to(device))
         if t.dtype == torch.float8_e4m3fn:
             s = self._tensor(name + "_scale_inv").float()
             if t.dim() == 3:

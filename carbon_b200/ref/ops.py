@@ -117,6 +117,44 @@ def dequant_fp8_blocks(q: torch.Tensor, s: torch.Tensor, block: int = 128) -> to
     return q.float() * sf
 
 
+# ----------------------------------------------------------------------------------------------------------------------
+# MXFP4 (OCP microscaling fp4): e2m1 elements, one UE8M0 power-of-two scale per 32 consecutive elements of a row.
+# The reference's routed experts are stored this way (fp8 activations x MXFP4 weights, UE8M0/32; moe_prefill.py:14-16).
+# ----------------------------------------------------------------------------------------------------------------------
+E2M1_VALUES = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0)      # magnitudes of codes 0..7; bit 3 is the sign
+
+
+def quant_mxfp4(w: torch.Tensor, block: int = 32) -> Tuple[torch.Tensor, torch.Tensor]:
+    """[N, K] -> (packed uint8 [N, K/2]: element 2i in the low nibble, 2i+1 in the high one; scale uint8 [N, K/32]:
+    biased exponent e+127 of the block scale 2^e, the smallest power of two with amax / 2^e <= 6).  Elements round
+    to the nearest e2m1 value (ties to the smaller magnitude)."""
+    N, K = w.shape
+    assert K % block == 0 and block % 2 == 0
+    wb = w.float().reshape(N, K // block, block)
+    amax = wb.abs().amax(-1)
+    m, ex = torch.frexp(amax / 6.0)                          # amax/6 = m * 2^ex, m in [0.5, 1)
+    e = torch.where(amax > 0, ex - (m == 0.5).to(ex.dtype), torch.zeros_like(ex)).clamp(-127, 127)
+    x = wb / torch.pow(2.0, e.float())[..., None]
+    grid = torch.tensor(E2M1_VALUES, dtype=torch.float32, device=w.device)
+    code = (x.abs()[..., None] - grid).abs().argmin(-1)      # first minimum: the smaller magnitude on a tie
+    nib = code | (((x < 0) & (code > 0)).long() << 3)
+    nib = nib.reshape(N, K)
+    packed = (nib[:, 0::2] | (nib[:, 1::2] << 4)).to(torch.uint8)
+    return packed.contiguous(), (e + 127).to(torch.uint8).contiguous()
+
+
+def dequant_mxfp4(packed: torch.Tensor, scale: torch.Tensor, block: int = 32) -> torch.Tensor:
+    """Inverse of ``quant_mxfp4``: -> fp32 [N, K]."""
+    N = packed.shape[0]
+    K = packed.shape[1] * 2
+    p = packed.long()
+    nib = torch.stack([p & 0xF, p >> 4], dim=-1).reshape(N, K)
+    grid = torch.tensor(E2M1_VALUES, dtype=torch.float32, device=packed.device)
+    v = grid[nib & 7] * torch.where((nib & 8) != 0, -1.0, 1.0)
+    s = torch.pow(2.0, scale.float() - 127.0).repeat_interleave(block, dim=1)
+    return v * s
+
+
 def fp8_gemm(a_q, a_s, b_q, b_s) -> torch.Tensor:
     """Block-scaled fp8 GEMM oracle: dequantise both operands and multiply in fp32. Returns [M, N] fp32."""
     return dequant_fp8_rows(a_q, a_s) @ dequant_fp8_blocks(b_q, b_s).t()

@@ -39,3 +39,27 @@ def test_checkpoint_roundtrip_and_engine(tmp_path):
     st = {n: CheckpointSource(cfg, str(tmp_path / "ckpt0")).get(n, "cpu") for n in w}
     e2 = Engine(cfg, "cpu", source=WeightSource(cfg, state=st), num_pages=8, page_size=16)
     assert e1.generate(prompts, 4) == e2.generate(prompts, 4)
+
+
+def test_mxfp4_experts_checkpoint(tmp_path):
+    """Routed experts stored as MXFP4 (e2m1 + UE8M0 per 32) load as their exact values, for stacked and per-expert
+    storage, and the engine served from that checkpoint equals the engine over the same values in memory; the V4
+    layout's grouped output projection (wo_b) is stored in fp8."""
+    from carbon_b200.config import tiny_v4_config
+
+    cfg = tiny_v4_config()
+    w = init_weights(cfg, seed=0)
+    for per_expert in (False, True):
+        d = tmp_path / f"mx{int(per_expert)}"
+        save_checkpoint(w, str(d), per_expert=per_expert, mxfp4_experts=True)
+        src = CheckpointSource(cfg, str(d))
+        for name in ("layers.0.ffn.experts.w1", "layers.1.ffn.experts.w2"):
+            exp = torch.stack([R.dequant_mxfp4(*R.quant_mxfp4(x)) for x in w[name]])
+            assert torch.equal(src.get(name, "cpu"), exp), name
+        got = src.get("layers.0.attn.wo_b.weight", "cpu")
+        assert torch.equal(got, R.dequant_fp8_blocks(*R.quant_fp8_blocks(w["layers.0.attn.wo_b.weight"])))
+    st = {n: CheckpointSource(cfg, str(tmp_path / "mx0")).get(n, "cpu") for n in w}
+    prompts = [[5, 6, 7, 8, 9] * 8]
+    e1 = Engine(cfg, "cpu", source=CheckpointSource(cfg, str(tmp_path / "mx0")), num_pages=8, page_size=16)
+    e2 = Engine(cfg, "cpu", source=WeightSource(cfg, state=st), num_pages=8, page_size=16)
+    assert e1.generate(prompts, 4) == e2.generate(prompts, 4)
