@@ -62,6 +62,17 @@ class ModelConfig:
     # the top-k selection is taken over the keys older than the window, so the two sets are disjoint
     # (reference: SWA window 128, per-row index width 512 top-k + 128 window; rehome_attn.py:8,17-19).  0: off.
     swa_window: int = 0
+    # Engram (hashed n-gram memory; reference layers 1 and 14, peer_read.py:15, dspd_w22/dspd/engram.py:259-268):
+    # each token's n-grams (orders engram_orders, engram_heads hash heads per order) index one row of a hashed table
+    # per column; the engram_dim-wide rows of all columns are concatenated, projected by wkv to one key per mHC stream
+    # plus one shared value, and every stream gets x_c += sigmoid(clamp(<rms(x_c)*q_w, rms(k_c)*k_w> / sqrt(D))) * value.
+    # The hash and the gate are this framework's own definitions (the reference's live in its sealed engine).
+    engram_layers: tuple = ()
+    engram_orders: tuple = (2, 3)
+    engram_heads: int = 12
+    engram_dim: int = 256
+    engram_rows: int = 4096            # rows per column (each column's modulus is the first prime >= this)
+    engram_clamp: float = 10.0
     # MoE
     n_routed_experts: int = 256
     n_activated_experts: int = 8
@@ -125,6 +136,24 @@ class ModelConfig:
         return layer >= self.n_dense_layers and self.n_routed_experts > 0
 
     @property
+    def engram_cols(self) -> int:
+        return len(self.engram_orders) * self.engram_heads
+
+    @property
+    def engram_primes(self) -> tuple:
+        """Modulus of each hash column: distinct primes >= engram_rows, in column order."""
+        out, n = [], max(2, self.engram_rows)
+        while len(out) < self.engram_cols:
+            if all(n % d for d in range(2, int(n ** 0.5) + 1)):
+                out.append(n)
+            n += 1
+        return tuple(out)
+
+    @property
+    def engram_table_rows(self) -> int:
+        return sum(self.engram_primes)
+
+    @property
     def softmax_scale(self) -> float:
         return self.qk_head_dim ** -0.5
 
@@ -163,6 +192,8 @@ class ModelConfig:
         if self.o_groups:
             assert self.n_heads % self.o_groups == 0 and self.o_lora_rank > 0
         assert self.swa_window >= 0
+        if self.engram_layers:
+            assert self.engram_dim % 32 == 0 and self.engram_cols > 0 and min(self.engram_orders) >= 1
 
 
 def tiny_config() -> ModelConfig:
@@ -198,19 +229,22 @@ def tiny_v4_config() -> ModelConfig:
     """The tiny CPU model in the DeepSeek-V4 attention layout: latent MQA (one 64-dim latent head with 16 RoPE dims),
     grouped low-rank output projection, sliding window 16, per-head sinks, DSA index sources, sqrt-softplus router."""
     return tiny_config().replace(attn_kind="latent_mqa", o_groups=2, o_lora_rank=64, swa_window=16, attn_sink=True,
-                                 index_sources=(0,), index_topk=16, score_func="sqrtsoftplus")
+                                 index_sources=(0,), index_topk=16, score_func="sqrtsoftplus", engram_layers=(1,),
+                                 engram_heads=2, engram_dim=64, engram_rows=97)
 
 
 def deepseek_v4_config() -> ModelConfig:
     """DeepSeek-V4.1-Flash-shaped model (the reference's target): 40 layers, hidden 5120, 64 heads of
     latent MQA over a 512-dim latent (64 RoPE dims), q_lora 1280, 8 output groups with o_lora 1024, window 128,
     indexer 32 heads x 128 top-512 on source layers 2, 8, 14, 384 experts top-6 (intermediate 2304, sqrt-softplus
-    router), mHC 4 streams.  Layer shapes only: the compressed KV pool, Engram and MXFP4 experts are not modelled."""
+    router), mHC 4 streams, Engram on layers 1 and 14 (24 hash columns of 256-dim rows).  The compressed KV pool is
+    not modelled (its keys come from the same latent cache); MXFP4 experts load through the checkpoint format."""
     return ModelConfig(
         vocab_size=129280, hidden_size=5120, n_layers=40, n_dense_layers=0, dense_intermediate=12288,
         n_heads=64, q_lora_rank=1280, kv_lora_rank=512, qk_nope_head_dim=448, qk_rope_head_dim=64, v_head_dim=512,
         max_position=65536, index_n_heads=32, index_head_dim=128, index_topk=512, index_sources=(2, 8, 14),
-        attn_sink=True, attn_kind="latent_mqa", o_groups=8, o_lora_rank=1024, swa_window=128,
+        attn_sink=True, attn_kind="latent_mqa", o_groups=8, o_lora_rank=1024, swa_window=128, engram_layers=(1, 14),
+        engram_orders=(2, 3), engram_heads=12, engram_dim=256, engram_rows=1 << 20,
         n_routed_experts=384, n_activated_experts=6, n_shared_experts=1, moe_intermediate=2304,
         score_func="sqrtsoftplus", route_scale=2.5,
     )

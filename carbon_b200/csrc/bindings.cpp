@@ -323,6 +323,32 @@ void sparse_mla(torch::Tensor q, torch::Tensor kv, torch::Tensor idx, double sca
                     int(q.size(2))));
 }
 
+// Engram row gather: ids [T, C] int32 global rows; data_ptrs / sf_ptrs uint64 [world] (fp8 rows [R_r, dim], UE8M0
+// bytes [R_r, dim/32] of each rank's shard); bounds int32 [world + 1] global row ranges -> out [T, C*dim] bf16
+void engram_gather(torch::Tensor ids, torch::Tensor data_ptrs, torch::Tensor sf_ptrs, torch::Tensor bounds,
+                   int64_t dim, torch::Tensor out) {
+  CHECK_CUDA(ids); CHECK_DT(ids, at::kInt); CHECK_CONTIG(ids); CHECK_DT(bounds, at::kInt); CHECK_CONTIG(out);
+  CHECK_DT(out, at::kBFloat16);
+  TORCH_CHECK(out.numel() == ids.numel() * dim, "engram_gather: out size");
+  c10::cuda::CUDAGuard g(ids.device());
+  CK(cb::engram_gather(ids.data_ptr<int>(), ids.size(0), ids.size(1), dim,
+                       reinterpret_cast<const uint64_t*>(data_ptrs.data_ptr()),
+                       reinterpret_cast<const uint64_t*>(sf_ptrs.data_ptr()), bounds.data_ptr<int>(),
+                       data_ptrs.numel(), out.data_ptr(), cur_stream()));
+}
+
+// Engram gate, in place on X [T, hc, D] bf16 with kv [T, (hc+1)*D] bf16; sumsq [T] fp32 <- new sum of squares
+void engram_gate(torch::Tensor X, torch::Tensor kv, torch::Tensor qw, torch::Tensor kw, double eps, double clamp,
+                 torch::Tensor sumsq) {
+  CHECK_CUDA(X); CHECK_DT(X, at::kBFloat16); CHECK_DT(kv, at::kBFloat16); CHECK_CONTIG(X); CHECK_CONTIG(kv);
+  CHECK_DT(qw, at::kFloat); CHECK_DT(kw, at::kFloat); CHECK_DT(sumsq, at::kFloat);
+  const int T = X.size(0), hc = X.size(1), D = X.size(2);
+  TORCH_CHECK(kv.size(0) == T && kv.size(1) == (hc + 1) * D, "engram_gate: kv shape");
+  c10::cuda::CUDAGuard g(X.device());
+  CK(cb::engram_gate(X.data_ptr(), kv.data_ptr(), qw.data_ptr<float>(), kw.data_ptr<float>(), T, hc, D, float(eps),
+                     float(clamp), sumsq.data_ptr<float>(), cur_stream()));
+}
+
 // decode-side DSA: q [T, H, 128] bf16, w [T, H] fp32, kc [S, 128] bf16, key_slots [T, L], n_keys [T] -> out [T, k]
 void indexer_topk(torch::Tensor q, torch::Tensor w, torch::Tensor kc, torch::Tensor key_slots, torch::Tensor n_keys,
                   torch::Tensor out) {
@@ -369,5 +395,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("indexer_logits", &indexer_logits);
   m.def("topk_mask", &topk_mask);
   m.def("sparse_mla", &sparse_mla);
+  m.def("engram_gather", &engram_gather);
+  m.def("engram_gate", &engram_gate);
   m.def("indexer_topk", &indexer_topk);
 }

@@ -81,4 +81,11 @@ cudaError_t sparse_mla(const void* q, int T, int H, const void* kv, int S, const
                        int n_splits, float* part_o, float* part_ml, void* out, int* status, cudaStream_t s,
                        const float* sink = nullptr, int D = 576);
 
+// Engram (engram.cu): fp8 row gather (UE8M0 per 32; table split over ranks by row ranges `bounds`, peer pointers)
+// and the fused per-stream gate + residual update + new sum of squares
+cudaError_t engram_gather(const int* ids, int T, int C, int dim, const uint64_t* data_ptrs, const uint64_t* sf_ptrs,
+                          const int* bounds, int world, void* out, cudaStream_t s);
+cudaError_t engram_gate(void* X, const void* kv, const float* qw, const float* kw, int T, int hc, int D, float eps,
+                        float clamp, float* sumsq, cudaStream_t s);
+
 }  // namespace cb

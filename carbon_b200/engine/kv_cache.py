@@ -33,7 +33,12 @@ class PagedLatentCache:
         if cfg.use_indexer:
             self.index_k = [torch.zeros(self.num_slots, cfg.index_head_dim, dtype=dtype, device=device)
                             if cfg.has_indexer(l) else None for l in range(n_layers)]
+        # token id of every slot (Engram hashes each token's preceding n-gram; decode reads them through key slots)
+        self.tok = torch.zeros(self.num_slots, dtype=torch.int32, device=device) if cfg.engram_layers else None
         self.alloc = BlockAllocator(num_pages)
+
+    def write_tokens(self, loc: torch.Tensor, ids: torch.Tensor) -> None:
+        self.tok.index_copy_(0, loc.long(), ids.to(torch.int32))
 
     def write_latent(self, layer: int, loc: torch.Tensor, rows: torch.Tensor) -> None:
         self.latent[layer].index_copy_(0, loc.long(), rows.to(self.latent[layer].dtype))

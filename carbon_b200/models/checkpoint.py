@@ -28,8 +28,8 @@ from ..config import ModelConfig
 from ..ref import ops as R
 from .weights import WeightSource
 
-FP8_SUFFIXES = ("wq_a.weight", "wq_b.weight", "wkv_a.weight", "wkv_b.weight", "wo.weight", "wo_b.weight", "ffn.w1",
-                "ffn.w2",
+FP8_SUFFIXES = ("wq_a.weight", "wq_b.weight", "wkv_a.weight", "wkv_b.weight", "wo.weight", "wo_b.weight",
+                "engram.wkv.weight", "ffn.w1", "ffn.w2",
                 "ffn.w3", "experts.w1", "experts.w2", "experts.w3", "shared.w1", "shared.w2", "shared.w3")
 _EXPERT_RE = re.compile(r"^(layers\.\d+\.ffn\.experts)\.(\d+)\.(w[123])$")
 
@@ -56,6 +56,9 @@ def save_checkpoint(state: Dict[str, torch.Tensor], path: str, shard_bytes: int 
             else:
                 out[name] = torch.stack([q for q, _ in qs])
                 out[name + "_scale"] = torch.stack([s for _, s in qs])
+        elif name.endswith("engram.table"):
+            # Engram rows: e4m3 with one UE8M0 byte per 32 elements (the reference's 256 e4m3 + UE8M0/32 rows)
+            out[name], out[name + "_sf32"] = R.quant_fp8_rows32(t.float())
         elif is_fp8_name(name):
             if t.dim() == 3:
                 mats = [(f"{name[:-3]}.{e}.{name[-2:]}" if per_expert else None, t[e]) for e in range(t.shape[0])]
@@ -147,6 +150,8 @@ class CheckpointSource(WeightSource):
             if t.dim() == 3:
                 return torch.stack([R.dequant_mxfp4(t[e].to(device), s[e].to(device)) for e in range(t.shape[0])])
             return R.dequant_mxfp4(t.to(device), s.to(device))
+        if t.dtype == torch.float8_e4m3fn and self.has(name + "_sf32"):        # Engram rows
+            return R.dequant_fp8_rows32(t.to(device), self._tensor(name + "_sf32").to(device))
         if t.dtype == torch.float8_e4m3fn:
             s = self._tensor(name + "_scale_inv").float()
             if t.dim() == 3:

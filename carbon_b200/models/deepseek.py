@@ -182,6 +182,59 @@ class DeepseekModel:
         self.n_weight_sets = len(built)
 
     # ------------------------------------------------------------------------------------------------------------------
+    def _load_engram(self, prefix: str, get):
+        """Engram weights: the hashed table (GPU: e4m3 rows + UE8M0 per 32, the gather kernel's format), the wkv
+        projection, the gate's q / k norm weights."""
+        E = Layer()
+        table = get(prefix + "table")
+        if self.on_gpu:
+            q, sf = R.quant_fp8_rows32(table)
+            E.data, E.sf = q.contiguous(), sf.contiguous()
+            E.data_ptrs = torch.tensor([E.data.data_ptr()], dtype=torch.int64, device=self.device)
+            E.sf_ptrs = torch.tensor([E.sf.data_ptr()], dtype=torch.int64, device=self.device)
+            E.bounds = torch.tensor([0, table.shape[0]], dtype=torch.int32, device=self.device)
+        else:
+            E.table = table
+        del table
+        E.wkv = Lin(get(prefix + "wkv.weight"), self.device, self.fp8)
+        E.qw = get(prefix + "q_weight").float().contiguous()
+        E.kw = get(prefix + "k_weight").float().contiguous()
+        return E
+
+    def engram(self, i: int, X: torch.Tensor, sumsq, fb: ForwardBatch, cache):
+        """Hashed n-gram memory on this rank's residual streams X [T_l, hc, D]: hash each token's preceding n-grams
+        (prefill: from the batch; decode: the cached token ids of the key slots), gather the table rows, project
+        (wkv) and gate every stream.  Returns (X, sumsq) updated."""
+        cfg, E, pc = self.cfg, self.layers[i].engram, self.pctx
+        lo, hi = pc.local
+        nmax = max(cfg.engram_orders)
+        dev = X.device
+        back = torch.arange(nmax, device=dev)
+        p = fb.pos[lo:hi].long()
+        if fb.is_prefill:
+            src = (torch.arange(lo, hi, device=dev)[:, None] - back[None, :]).clamp(min=0)
+            toks = fb.ids[src].long()
+        else:
+            j = p[:, None] - back[None, :]
+            slot = fb.key_slots[lo:hi].gather(1, j.clamp(min=0)).long()
+            toks = cache.tok[slot.clamp(min=0)].long()
+        window = torch.where(p[:, None] - back[None, :] >= 0, toks, -1)
+        rows = R.engram_hash_ids(window, cfg.engram_orders, cfg.engram_heads, cfg.engram_primes, cfg.vocab_size)
+        T = X.shape[0]
+        if not self.on_gpu:
+            kv = E.wkv(E.table[rows].reshape(T, -1))
+            Xn = R.engram_gate(X, kv, E.qw, E.kw, cfg.rms_eps, cfg.engram_clamp).to(X.dtype)
+            return Xn, (None if sumsq is None else Xn.float().pow(2).sum((1, 2)))
+        from ..ops._ext import ext
+
+        emb = torch.empty(T, cfg.engram_cols * cfg.engram_dim, dtype=torch.bfloat16, device=dev)
+        ext().engram_gather(rows.to(torch.int32).contiguous(), E.data_ptrs, E.sf_ptrs, E.bounds, cfg.engram_dim, emb)
+        kv = E.wkv(emb).contiguous()
+        X = X.contiguous()
+        ss = torch.empty(T, dtype=torch.float32, device=dev)
+        ext().engram_gate(X, kv, E.qw, E.kw, cfg.rms_eps, cfg.engram_clamp, ss)
+        return X, ss
+
     def _load_layer(self, i: int, get) -> Layer:
         cfg, dev, pc = self.cfg, self.device, self.pctx
         L = Layer()
@@ -227,6 +280,9 @@ class DeepseekModel:
             L.wo = Lin(wo[:, h0 * dvh:h1 * dvh].contiguous(), dev, self.fp8)
         L.sink = get(a + "sink")[h0:h1].float().contiguous() if cfg.attn_sink else None
         L.sink_all = get(a + "sink").float().contiguous().to(dev) if cfg.attn_sink else None     # every head
+        L.engram = None
+        if i in cfg.engram_layers:
+            L.engram = self._load_engram(p + "engram.", get)
         L.has_indexer = cfg.has_indexer(i)
         if L.has_indexer:
             ix = a + "indexer."
@@ -469,6 +525,11 @@ class DeepseekModel:
                     cand = (nk_l - W).clamp(min=0).to(torch.int32).contiguous()      # keys older than the window
                     sel = A.indexer_topk(qi, wi, cache.index_k[i], ks_l.contiguous(), cand, cfg.index_topk)
                     sel = sel if local else pc.gather_rows(sel)
+                if self.trace is not None and fb.is_prefill:
+                    # selected key positions (debugging: lets an oracle follow this selection exactly)
+                    inv = torch.full((int(fb.out_loc.max()) + 1,), -1, dtype=torch.long, device=dev)
+                    inv[fb.out_loc.long()] = fb.pos.long()
+                    self._tr(f"{i}.dsa_pos", torch.where(sel >= 0, inv[sel.long().clamp(min=0)], -1))
                 self._dsa[i] = sel
             else:
                 sel = self._dsa[src]                # selection shared with the index-source layer
@@ -635,8 +696,13 @@ class DeepseekModel:
         self._dsa = {}                 # DSA selections of this forward's index-source layers
         with region("embed"):
             X, sumsq = self.embed_tokens(fb.ids)
+        if cfg.engram_layers:
+            cache.write_tokens(fb.out_loc, fb.ids)
         for i in range(cfg.n_layers):
             L = self.layers[i]
+            if L.engram is not None:
+                with region("engram"):
+                    X, sumsq = self.engram(i, X, sumsq, fb, cache)
             with region("mhc.coeffs"):
                 pre, post, comb = self.hc_coeffs(X, sumsq, L.attn_hc)
             with region("mhc.pre_norm"):

@@ -39,6 +39,11 @@ def param_shapes(cfg: ModelConfig) -> "OrderedDict[str, Tuple[Tuple[int, ...], s
             p[L + sub + ".base"] = ((cfg.hc_mix_dim,), "normal")
             p[L + sub + ".scale"] = ((3,), "ones")
         p[L + "attn_norm.weight"] = ((D,), "ones")
+        if i in cfg.engram_layers:
+            p[L + "engram.table"] = ((cfg.engram_table_rows, cfg.engram_dim), "normal")
+            p[L + "engram.wkv.weight"] = (((hc + 1) * D, cfg.engram_cols * cfg.engram_dim), "normal")
+            p[L + "engram.q_weight"] = ((D,), "ones")
+            p[L + "engram.k_weight"] = ((D,), "ones")
         if cfg.q_lora_rank > 0:
             p[L + "attn.wq_a.weight"] = ((cfg.q_lora_rank, D), "normal")
             p[L + "attn.q_norm.weight"] = ((cfg.q_lora_rank,), "ones")
@@ -116,6 +121,7 @@ class RefModel:
         self.cfg = cfg
         self.w = {k: v.float() for k, v in weights.items()}
         self.forced_routing = None   # {layer: ids [T, k]}: use these expert choices instead of the router's top-k
+        self.forced_dsa = None       # {layer: positions [T, topk] (-1 pad)}: use this DSA selection instead
         self._dsa = {}               # DSA selection of each index-source layer in the current forward
 
     # -- sublayers -------------------------------------------------------------------------------------------------
@@ -157,6 +163,11 @@ class RefModel:
             if window is not None:                      # top-k over the keys older than the window
                 logits = logits.masked_fill(window, float("-inf"))
             allowed = ops.topk_mask(logits, pos, pos, cfg.index_topk)
+            if self.forced_dsa is not None and i in self.forced_dsa:
+                sel = self.forced_dsa[i].long()
+                allowed = torch.zeros(T, T + 1, dtype=torch.bool)          # column T collects the -1 pads
+                allowed.scatter_(1, torch.where(sel >= 0, sel, T), True)
+                allowed = allowed[:, :T]
             if window is not None:
                 allowed = allowed & ~window
             self._dsa[i] = allowed
@@ -245,9 +256,25 @@ class RefModel:
         X = w["embed.weight"][ids.long()][:, None, :].expand(T, cfg.hc_mult, cfg.hidden_size).clone()
         for i in range(cfg.n_layers):
             L = f"layers.{i}."
+            if i in cfg.engram_layers:
+                X = self.engram(i, X, ids, pos)
             X = self.hc_sublayer(X, L + "attn_hc", w[L + "attn_norm.weight"], lambda y: self.attention(i, y, pos))
             X = self.hc_sublayer(X, L + "ffn_hc", w[L + "ffn_norm.weight"], lambda y: self.ffn(i, y))
         return self.head(X)
+
+    def engram(self, i: int, X: torch.Tensor, ids: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
+        """Hashed n-gram memory on the residual streams (one sequence: ids in position order)."""
+        cfg, w = self.cfg, self.w
+        L = f"layers.{i}.engram."
+        T = ids.shape[0]
+        nmax = max(cfg.engram_orders)
+        back = torch.arange(nmax)
+        src = torch.arange(T)[:, None] - back[None, :]
+        window = torch.where(pos[:, None] - back[None, :] >= 0, ids.long()[src.clamp(min=0)], -1)
+        rows = ops.engram_hash_ids(window, cfg.engram_orders, cfg.engram_heads, cfg.engram_primes, cfg.vocab_size)
+        emb = w[L + "table"][rows].reshape(T, -1)                                  # [T, cols * dim]
+        kv = emb @ w[L + "wkv.weight"].t()
+        return ops.engram_gate(X, kv, w[L + "q_weight"], w[L + "k_weight"], cfg.rms_eps, cfg.engram_clamp)
 
     def head(self, X: torch.Tensor) -> torch.Tensor:
         cfg, w = self.cfg, self.w

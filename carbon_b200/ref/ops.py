@@ -155,6 +155,22 @@ def dequant_mxfp4(packed: torch.Tensor, scale: torch.Tensor, block: int = 32) ->
     return v * s
 
 
+def quant_fp8_rows32(w: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """[R, K] -> (e4m3 [R, K], UE8M0 biased exponents uint8 [R, K/32]): one power-of-two scale per 32 elements,
+    the smallest with amax / 2^e <= 448 (the Engram table row format: 256 e4m3 + UE8M0/32)."""
+    R_, K = w.shape
+    wb = w.float().reshape(R_, K // 32, 32)
+    amax = wb.abs().amax(-1)
+    m, ex = torch.frexp(amax / FP8_MAX)
+    e = torch.where(amax > 0, ex - (m == 0.5).to(ex.dtype), torch.full_like(ex, -127)).clamp(-127, 127)
+    q = (wb / torch.pow(2.0, e.float())[..., None]).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
+    return q.reshape(R_, K).contiguous(), (e + 127).to(torch.uint8).contiguous()
+
+
+def dequant_fp8_rows32(q: torch.Tensor, sf: torch.Tensor) -> torch.Tensor:
+    return q.float() * torch.pow(2.0, sf.float() - 127.0).repeat_interleave(32, dim=1)
+
+
 def fp8_gemm(a_q, a_s, b_q, b_s) -> torch.Tensor:
     """Block-scaled fp8 GEMM oracle: dequantise both operands and multiply in fp32. Returns [M, N] fp32."""
     return dequant_fp8_rows(a_q, a_s) @ dequant_fp8_blocks(b_q, b_s).t()
@@ -286,3 +302,44 @@ def topk_mask(logits: torch.Tensor, q_pos: torch.Tensor, k_pos: torch.Tensor, to
     m = torch.zeros_like(causal)
     m.scatter_(1, idx, True)
     return m & causal
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# Engram: hashed n-gram memory
+# ----------------------------------------------------------------------------------------------------------------------
+ENGRAM_MULT = 1000003          # hash multiplier (odd, < 2^20 so every step fits int64)
+
+
+def engram_hash_ids(window: torch.Tensor, orders, heads: int, primes, vocab_size: int) -> torch.Tensor:
+    """window [T, nmax] int64: column i = the token i positions back (i = 0: the token itself), -1 before the
+    sequence start.  Column c = (order orders[c // heads], head c % heads) hashes the `order` most recent tokens:
+    h = 0; for each token u (most recent first): h = ((h * MULT) ^ (u' + 7919 * (c + 1))) & (2^31 - 1), with
+    u' = u + 1 (0 for the padding before the sequence start); row = h % primes[c] + (rows of earlier columns).
+    Returns int64 [T, n_cols] global table rows."""
+    T = window.shape[0]
+    cols = []
+    base = 0
+    w = torch.where(window >= 0, window + 1, torch.zeros_like(window)).long()
+    for c in range(len(orders) * heads):
+        n = orders[c // heads]
+        h = torch.zeros(T, dtype=torch.long, device=window.device)
+        for i in range(n):
+            h = ((h * ENGRAM_MULT) ^ (w[:, i] + 7919 * (c + 1))) & 0x7FFFFFFF
+        cols.append(h % primes[c] + base)
+        base += primes[c]
+    return torch.stack(cols, dim=1)
+
+
+def engram_gate(X: torch.Tensor, kv: torch.Tensor, q_w: torch.Tensor, k_w: torch.Tensor, eps: float,
+                clamp: float) -> torch.Tensor:
+    """X [T, hc, D] residual streams, kv [T, (hc + 1) * D] = per-stream keys then the shared value.
+    X_c + sigmoid(clamp(<rms(X_c) * q_w, rms(k_c) * k_w> / sqrt(D), +-clamp)) * value."""
+    T, hc, D = X.shape
+    Xf = X.float()
+    k = kv[:, :hc * D].float().view(T, hc, D)
+    v = kv[:, hc * D:].float()
+    xn = Xf * torch.rsqrt(Xf.pow(2).mean(-1, keepdim=True) + eps) * q_w.float()
+    kn = k * torch.rsqrt(k.pow(2).mean(-1, keepdim=True) + eps) * k_w.float()
+    s = (xn * kn).sum(-1) / math.sqrt(D)
+    g = torch.sigmoid(s.clamp(-clamp, clamp))                                  # [T, hc]
+    return Xf + g[..., None] * v[:, None, :]

@@ -58,6 +58,8 @@ def test_mxfp4_experts_checkpoint(tmp_path):
             assert torch.equal(src.get(name, "cpu"), exp), name
         got = src.get("layers.0.attn.wo_b.weight", "cpu")
         assert torch.equal(got, R.dequant_fp8_blocks(*R.quant_fp8_blocks(w["layers.0.attn.wo_b.weight"])))
+        tab = w["layers.1.engram.table"]           # Engram rows: e4m3 + UE8M0 per 32
+        assert torch.equal(src.get("layers.1.engram.table", "cpu"), R.dequant_fp8_rows32(*R.quant_fp8_rows32(tab)))
     st = {n: CheckpointSource(cfg, str(tmp_path / "mx0")).get(n, "cpu") for n in w}
     prompts = [[5, 6, 7, 8, 9] * 8]
     e1 = Engine(cfg, "cpu", source=CheckpointSource(cfg, str(tmp_path / "mx0")), num_pages=8, page_size=16)

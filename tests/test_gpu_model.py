@@ -15,7 +15,8 @@ from carbon_b200.ref.model import RefModel, init_weights
 
 pytestmark = pytest.mark.gpu
 
-FP8_NAMES = ("wq_a.weight", "wq_b.weight", "wkv_a.weight", "wkv_b.weight", "wo.weight", "wo_b.weight", "ffn.w1", "ffn.w2",
+FP8_NAMES = ("wq_a.weight", "wq_b.weight", "wkv_a.weight", "wkv_b.weight", "wo.weight", "wo_b.weight",
+             "engram.wkv.weight", "ffn.w1", "ffn.w2",
              "ffn.w3", "experts.w1", "experts.w2", "experts.w3", "shared.w1", "shared.w2", "shared.w3")
 
 
@@ -26,7 +27,9 @@ def _rel(a, b):
 def fp8_roundtrip(w):
     out = {}
     for k, v in w.items():
-        if k.endswith(FP8_NAMES):
+        if k.endswith("engram.table"):
+            out[k] = R.dequant_fp8_rows32(*R.quant_fp8_rows32(v))
+        elif k.endswith(FP8_NAMES):
             if v.dim() == 3:
                 out[k] = torch.stack([R.dequant_fp8_blocks(*R.quant_fp8_blocks(x)) for x in v])
             else:
@@ -117,10 +120,12 @@ def test_smoke_entry():
 
 def _v4_cfg(n_layers=2):
     """The V4 attention layout at kernel-compatible sizes: latent MQA over a 512-dim latent (64 RoPE dims), 16 heads
-    in 4 output groups (o_lora 256), window 64 + top-128 over older keys, sinks, sqrt-softplus router."""
+    in 4 output groups (o_lora 256), window 64 + top-128 over older keys, sinks, sqrt-softplus router, Engram on
+    layer 1 (4 hash columns of 256-dim e4m3 rows)."""
     return small_gpu_config().replace(n_layers=n_layers, n_routed_experts=8, n_activated_experts=2, vocab_size=2048,
                                       attn_kind="latent_mqa", o_groups=4, o_lora_rank=256, swa_window=64,
-                                      attn_sink=True, index_topk=128, score_func="sqrtsoftplus")
+                                      attn_sink=True, index_topk=128, score_func="sqrtsoftplus", engram_layers=(1,),
+                                      engram_heads=2, engram_dim=256, engram_rows=997)
 
 
 @pytest.mark.parametrize("plen", [48, 300])
@@ -134,7 +139,9 @@ def test_v4_latent_mqa_model_vs_oracle(plen):
     eng.model.trace = []
     r = eng.add_request(prompt.tolist())
     got = eng.prefill([r])[0].float().cpu()
+    # the oracle follows the GPU's expert choices and DSA selection (near-ties are not numerics errors)
     ref.forced_routing = {int(k.split(".")[0]): v.long() for k, v in eng.model.trace if k.endswith("router_ids")}
+    ref.forced_dsa = {int(k.split(".")[0]): v.long() for k, v in eng.model.trace if k.endswith("dsa_pos")}
     exp = ref.forward(prompt)[-1]
     assert _rel(got, exp) < 0.15, _rel(got, exp)
     assert torch.corrcoef(torch.stack([got, exp]))[0, 1] > 0.98
@@ -167,3 +174,33 @@ def test_v4_latent_mqa_cuda_graph_decode_matches_eager():
     assert o1 == o2
     for a, b in zip(h1, h2):
         assert torch.allclose(a, b, atol=1e-3, rtol=1e-3)
+
+
+def test_engram_kernels_vs_oracle():
+    """Row gather (e4m3 + UE8M0/32, two row shards addressed through the pointer table) and the fused gate against
+    the fp32 oracle of the same op."""
+    from carbon_b200.ops._ext import ext
+
+    torch.manual_seed(0)
+    R_, dim, T, C, hc, D = 1000, 256, 77, 6, 4, 1024
+    table = torch.randn(R_, dim) * 0.05
+    q, sf = R.quant_fp8_rows32(table)
+    ref_tab = R.dequant_fp8_rows32(q, sf)
+    cut = 613                                   # two shards: rows [0, 613) and [613, 1000)
+    parts = [(q[:cut].cuda(), sf[:cut].cuda()), (q[cut:].cuda(), sf[cut:].cuda())]
+    dp = torch.tensor([p[0].data_ptr() for p in parts], dtype=torch.int64, device="cuda")
+    sp = torch.tensor([p[1].data_ptr() for p in parts], dtype=torch.int64, device="cuda")
+    bounds = torch.tensor([0, cut, R_], dtype=torch.int32, device="cuda")
+    ids = torch.randint(0, R_, (T, C), dtype=torch.int32)
+    out = torch.empty(T, C * dim, dtype=torch.bfloat16, device="cuda")
+    ext().engram_gather(ids.cuda(), dp, sp, bounds, dim, out)
+    assert torch.equal(out.float().cpu(), ref_tab[ids.long()].reshape(T, -1).to(torch.bfloat16).float())
+    X = torch.randn(T, hc, D).to(torch.bfloat16)
+    kv = torch.randn(T, (hc + 1) * D).to(torch.bfloat16)
+    qw, kw = torch.rand(D) + 0.5, torch.rand(D) + 0.5
+    ref = R.engram_gate(X.float(), kv.float(), qw, kw, 1e-6, 10.0)
+    Xg = X.cuda().contiguous()
+    ss = torch.empty(T, device="cuda")
+    ext().engram_gate(Xg, kv.cuda(), qw.cuda(), kw.cuda(), 1e-6, 10.0, ss)
+    assert _rel(Xg.cpu(), ref) < 1e-2
+    assert _rel(ss.cpu(), Xg.float().pow(2).sum((1, 2)).cpu()) < 1e-4
