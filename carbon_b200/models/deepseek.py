@@ -186,8 +186,28 @@ class DeepseekModel:
         """Engram weights: the hashed table (GPU: e4m3 rows + UE8M0 per 32, the gather kernel's format), the wkv
         projection, the gate's q / k norm weights."""
         E = Layer()
+        cfg, pc = self.cfg, self.pctx
         table = get(prefix + "table")
-        if self.on_gpu:
+        if self.on_gpu and getattr(pc, "heap", None) is not None and pc.world > 1:
+            # split by whole hash columns over the ranks, each shard in the symmetric heap: the gather kernel reads a
+            # row from its owner's HBM over NVLink (no table replica, no lookup collective)
+            cb = [0]
+            for pr in cfg.engram_primes:
+                cb.append(cb[-1] + pr)
+            C, W = cfg.engram_cols, pc.world
+            cpr = (C + W - 1) // W
+            bounds = [cb[min(C, r * cpr)] for r in range(W)] + [cb[C]]
+            rows_max = max(bounds[r + 1] - bounds[r] for r in range(W))
+            lo, hi = bounds[pc.rank], bounds[pc.rank + 1]
+            q, sf = R.quant_fp8_rows32(table[lo:hi])
+            bd = pc.heap.alloc((max(rows_max, 1), cfg.engram_dim), torch.float8_e4m3fn)
+            bs = pc.heap.alloc((max(rows_max, 1), cfg.engram_dim // 32), torch.uint8)
+            bd.local[:hi - lo].copy_(q)
+            bs.local[:hi - lo].copy_(sf)
+            E.shards = (bd, bs)
+            E.data_ptrs, E.sf_ptrs = bd.peers, bs.peers
+            E.bounds = torch.tensor(bounds, dtype=torch.int32, device=self.device)
+        elif self.on_gpu:
             q, sf = R.quant_fp8_rows32(table)
             E.data, E.sf = q.contiguous(), sf.contiguous()
             E.data_ptrs = torch.tensor([E.data.data_ptr()], dtype=torch.int64, device=self.device)

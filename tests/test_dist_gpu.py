@@ -34,6 +34,15 @@ def _cfg():
                                       index_topk=4096)
 
 
+def _cfg_v4():
+    """The V4 layout with the same discrete-choice safeguards (all experts, no pruning top-k): latent MQA over the
+    token/head all-to-all, grouped output projection (one group per rank), window, sinks, Engram on layer 1 with its
+    table split over the two ranks' heaps (fused) or replicated (NCCL)."""
+    return _cfg().replace(attn_kind="latent_mqa", o_groups=2, o_lora_rank=256, swa_window=64, attn_sink=True,
+                          score_func="sqrtsoftplus", engram_layers=(1,), engram_heads=2, engram_dim=256,
+                          engram_rows=997)
+
+
 def _prompts(cfg):
     g = torch.Generator().manual_seed(5)
     return [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (60, 300, 130)]
@@ -50,7 +59,7 @@ def _run_forced(eng, prompts, steps=4):
     return hist
 
 
-def _worker(rank, world, port, comm, q, attn_dp=False):
+def _worker(rank, world, port, comm, q, attn_dp=False, v4=False):
     from datetime import timedelta
 
     from carbon_b200.engine.engine import Engine
@@ -67,7 +76,7 @@ def _worker(rank, world, port, comm, q, attn_dp=False):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
     ok = False
     try:
-        cfg = _cfg()
+        cfg = _cfg_v4() if v4 else _cfg()
         w = init_weights(cfg, seed=0)
         if comm == "fused":
             pctx = FusedCtx(rank, world, heap_bytes=1 << 30, max_tokens=1024, max_seq=512, attn_dp=attn_dp)
@@ -90,13 +99,14 @@ def _worker(rank, world, port, comm, q, attn_dp=False):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("comm,attn_dp", [("fused", False), ("nccl", False), ("fused", True), ("nccl", True)])
-def test_two_gpu_engine_matches_single_gpu(comm, attn_dp):
+@pytest.mark.parametrize("comm,attn_dp,v4", [("fused", False, False), ("nccl", False, False), ("fused", True, False),
+                                             ("nccl", True, False), ("fused", False, True), ("fused", True, True)])
+def test_two_gpu_engine_matches_single_gpu(comm, attn_dp, v4):
     from carbon_b200.engine.engine import Engine
     from carbon_b200.models.weights import WeightSource
     from carbon_b200.ref.model import init_weights
 
-    cfg = _cfg()
+    cfg = _cfg_v4() if v4 else _cfg()
     w = init_weights(cfg, seed=0)
     single = Engine(cfg, device="cuda:0", source=WeightSource(cfg, state=w), num_pages=64, page_size=64)
     hist_ref = _run_forced(single, _prompts(cfg))
@@ -105,7 +115,7 @@ def test_two_gpu_engine_matches_single_gpu(comm, attn_dp):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, comm, q, attn_dp)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, comm, q, attn_dp, v4)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=420) for _ in range(2)]
