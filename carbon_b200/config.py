@@ -73,6 +73,10 @@ class ModelConfig:
     engram_dim: int = 256
     engram_rows: int = 4096            # rows per column (each column's modulus is the first prime >= this)
     engram_clamp: float = 10.0
+    # multimodal: tokens with this id are image tokens; they rank experts with a second router bias
+    # (ffn.gate.bias_img) and take no Engram update (cuda_moe_front.py:265-269, dspd_w22/dspd/engram.py:261).
+    # -1: text only.
+    image_token_id: int = -1
     # MoE
     n_routed_experts: int = 256
     n_activated_experts: int = 8

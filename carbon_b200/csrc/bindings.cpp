@@ -87,13 +87,17 @@ void rope(torch::Tensor x, int64_t off, int64_t dim, torch::Tensor cos_sin, torc
                       cos_sin.data_ptr<float>(), pos.data_ptr<int>(), inverse, cur_stream()));
 }
 
+// bias_img / tok / img_id (optional): tokens with tok[t] == img_id rank with bias_img instead of bias
 void router_topk(torch::Tensor logits, c10::optional<torch::Tensor> bias, int64_t k, int64_t score, bool norm,
-                 double route_scale, torch::Tensor w, torch::Tensor ids) {
+                 double route_scale, torch::Tensor w, torch::Tensor ids, c10::optional<torch::Tensor> bias_img,
+                 c10::optional<torch::Tensor> tok, int64_t img_id) {
   CHECK_CUDA(logits); CHECK_DT(logits, at::kFloat); CHECK_CONTIG(logits);
   CHECK_DT(w, at::kFloat); CHECK_DT(ids, at::kInt);
+  if (tok.has_value() && tok->defined()) { CHECK_DT((*tok), at::kInt); CHECK_CONTIG((*tok)); }
   c10::cuda::CUDAGuard g(logits.device());
   CK(cb::router_topk(logits.data_ptr<float>(), ptr_or_null<const float>(bias), logits.size(0), logits.size(1), k,
-                     score, norm, float(route_scale), w.data_ptr<float>(), ids.data_ptr<int>(), cur_stream()));
+                     score, norm, float(route_scale), w.data_ptr<float>(), ids.data_ptr<int>(), cur_stream(),
+                     ptr_or_null<const float>(bias_img), ptr_or_null<const int>(tok), int(img_id)));
 }
 
 void moe_layout(torch::Tensor ids, int64_t E, torch::Tensor slot_pos, torch::Tensor row_src,
@@ -339,14 +343,15 @@ void engram_gather(torch::Tensor ids, torch::Tensor data_ptrs, torch::Tensor sf_
 
 // Engram gate, in place on X [T, hc, D] bf16 with kv [T, (hc+1)*D] bf16; sumsq [T] fp32 <- new sum of squares
 void engram_gate(torch::Tensor X, torch::Tensor kv, torch::Tensor qw, torch::Tensor kw, double eps, double clamp,
-                 torch::Tensor sumsq) {
+                 torch::Tensor sumsq, c10::optional<torch::Tensor> tok, int64_t img_id) {
   CHECK_CUDA(X); CHECK_DT(X, at::kBFloat16); CHECK_DT(kv, at::kBFloat16); CHECK_CONTIG(X); CHECK_CONTIG(kv);
   CHECK_DT(qw, at::kFloat); CHECK_DT(kw, at::kFloat); CHECK_DT(sumsq, at::kFloat);
   const int T = X.size(0), hc = X.size(1), D = X.size(2);
   TORCH_CHECK(kv.size(0) == T && kv.size(1) == (hc + 1) * D, "engram_gate: kv shape");
   c10::cuda::CUDAGuard g(X.device());
   CK(cb::engram_gate(X.data_ptr(), kv.data_ptr(), qw.data_ptr<float>(), kw.data_ptr<float>(), T, hc, D, float(eps),
-                     float(clamp), sumsq.data_ptr<float>(), cur_stream()));
+                     float(clamp), sumsq.data_ptr<float>(), cur_stream(), ptr_or_null<const int>(tok),
+                     int(img_id)));
 }
 
 // decode-side DSA: q [T, H, 128] bf16, w [T, H] fp32, kc [S, 128] bf16, key_slots [T, L], n_keys [T] -> out [T, k]

@@ -10,7 +10,7 @@
 //
 // engram_gate: X[t, s, :] += sigmoid(clamp(<rms(X_s) * q_w, rms(k_s) * k_w> / sqrt(D), +-clamp)) * v for every mHC
 //   stream s, with kv[t] = [k_0 .. k_{hc-1} | v]; writes the new sum of squares of X[t] (the mHC statistics input).
-//   One CTA per token.
+//   Tokens whose id is the image token (optional) are left unchanged.  One CTA per token.
 #include <cuda_bf16.h>
 #include <cuda_fp8.h>
 #include <cstdint>
@@ -83,9 +83,11 @@ __device__ __forceinline__ float block_sum_256(float v, float* red) {
 
 __global__ void engram_gate_kernel(__nv_bfloat16* __restrict__ X, const __nv_bfloat16* __restrict__ kv,
                                    const float* __restrict__ qw, const float* __restrict__ kw, int hc, int D,
-                                   float eps, float clamp, float* __restrict__ sumsq) {
+                                   float eps, float clamp, float* __restrict__ sumsq, const int* __restrict__ tok,
+                                   int img_id) {
   __shared__ float red[33];
   const int t = blockIdx.x;
+  const bool skip = tok != nullptr && tok[t] == img_id;          // image tokens take no n-gram update
   const __nv_bfloat16* kvt = kv + size_t(t) * (hc + 1) * D;
   const __nv_bfloat16* v = kvt + size_t(hc) * D;
   float ss_new = 0.f;
@@ -104,7 +106,7 @@ __global__ void engram_gate_kernel(__nv_bfloat16* __restrict__ X, const __nv_bfl
     dot = block_sum_256(dot, red);
     float z = dot * rsqrtf(sx / D + eps) * rsqrtf(sk / D + eps) * rsqrtf(float(D));
     z = fminf(fmaxf(z, -clamp), clamp);
-    const float g = 1.f / (1.f + __expf(-z));
+    const float g = skip ? 0.f : 1.f / (1.f + __expf(-z));
     for (int i = threadIdx.x; i < D; i += blockDim.x) {
       const __nv_bfloat16 nx = __float2bfloat16_rn(__bfloat162float(x[i]) + g * __bfloat162float(v[i]));
       x[i] = nx;
@@ -117,10 +119,11 @@ __global__ void engram_gate_kernel(__nv_bfloat16* __restrict__ X, const __nv_bfl
 }
 
 cudaError_t engram_gate(void* X, const void* kv, const float* qw, const float* kw, int T, int hc, int D, float eps,
-                        float clamp, float* sumsq, cudaStream_t s) {
+                        float clamp, float* sumsq, cudaStream_t s, const int* tok, int img_id) {
   if (T == 0) return cudaSuccess;
   engram_gate_kernel<<<T, 256, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(X),
-                                       reinterpret_cast<const __nv_bfloat16*>(kv), qw, kw, hc, D, eps, clamp, sumsq);
+                                       reinterpret_cast<const __nv_bfloat16*>(kv), qw, kw, hc, D, eps, clamp, sumsq,
+                                       tok, img_id);
   return cudaGetLastError();
 }
 

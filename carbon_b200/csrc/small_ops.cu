@@ -255,12 +255,16 @@ cudaError_t rope_inplace(void* x, int T, int64_t stride_t, int64_t stride_h, int
 // w = act[picked]; renormalise (optional); x route_scale.  E <= 1024, k <= 16.
 // score: 0 sigmoid, 1 sqrt(softplus), 2 softmax.
 // ---------------------------------------------------------------------------------------------------------------
+// Multimodal: when `bias_img` is given, tokens whose id (tok[t]) equals img_id rank with bias_img instead of bias
+// (the reference switches to a vision-language bias for image tokens; cuda_moe_front.py:265-269).
 template <int EPL>  // experts per lane
 __global__ void router_kernel(const float* __restrict__ logits, const float* __restrict__ bias, int T, int E, int k,
                               int score, int norm, float route_scale, float* __restrict__ w_out,
-                              int* __restrict__ id_out) {
+                              int* __restrict__ id_out, const float* __restrict__ bias_img,
+                              const int* __restrict__ tok, int img_id) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= T) return;
+  if (bias_img != nullptr && tok != nullptr && tok[warp] == img_id) bias = bias_img;
   const float* l = logits + size_t(warp) * E;
   float act[EPL], key[EPL];
   float mx = -INFINITY;
@@ -320,11 +324,13 @@ __global__ void router_kernel(const float* __restrict__ logits, const float* __r
   }
 }
 cudaError_t router_topk(const float* logits, const float* bias, int T, int E, int k, int score, bool norm,
-                        float route_scale, float* w, int* ids, cudaStream_t s) {
+                        float route_scale, float* w, int* ids, cudaStream_t s, const float* bias_img,
+                        const int* tok, int img_id) {
   if (T == 0) return cudaSuccess;
   if (k > 32 || E > 1024) return cudaErrorInvalidValue;
   const int blocks = ceil_div(T * 32, 256);
-#define CB_ROUTER(N) router_kernel<N><<<blocks, 256, 0, s>>>(logits, bias, T, E, k, score, norm ? 1 : 0, route_scale, w, ids)
+#define CB_ROUTER(N) router_kernel<N><<<blocks, 256, 0, s>>>(logits, bias, T, E, k, score, norm ? 1 : 0, route_scale, w, \
+                                                            ids, bias_img, tok, img_id)
   if (E <= 64) CB_ROUTER(2);
   else if (E <= 128) CB_ROUTER(4);
   else if (E <= 256) CB_ROUTER(8);

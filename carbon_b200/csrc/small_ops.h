@@ -17,7 +17,8 @@ cudaError_t sf_pad(uint32_t* sf, int M, int K, cudaStream_t s);
 cudaError_t rope_inplace(void* x, int T, int64_t stride_t, int64_t stride_h, int H, int off, int dim,
                          const float* cos_sin, const int* pos, bool inverse, cudaStream_t s);
 cudaError_t router_topk(const float* logits, const float* bias, int T, int E, int k, int score, bool norm,
-                        float route_scale, float* w, int* ids, cudaStream_t s);
+                        float route_scale, float* w, int* ids, cudaStream_t s,
+                        const float* bias_img = nullptr, const int* tok = nullptr, int img_id = -1);
 cudaError_t moe_layout(const int* ids, int T, int k, int E, int max_blocks, int* slot_pos, int* row_src,
                        int* m_block_expert, int* num_blocks, int* counts, cudaStream_t s, int align, int* scratch);
 cudaError_t moe_combine(const void* Y, int ldy, const float* w, const int* slot_pos, int T, int k, const void* add,
@@ -86,6 +87,6 @@ cudaError_t sparse_mla(const void* q, int T, int H, const void* kv, int S, const
 cudaError_t engram_gather(const int* ids, int T, int C, int dim, const uint64_t* data_ptrs, const uint64_t* sf_ptrs,
                           const int* bounds, int world, void* out, cudaStream_t s);
 cudaError_t engram_gate(void* X, const void* kv, const float* qw, const float* kw, int T, int hc, int D, float eps,
-                        float clamp, float* sumsq, cudaStream_t s);
+                        float clamp, float* sumsq, cudaStream_t s, const int* tok = nullptr, int img_id = -1);
 
 }  // namespace cb

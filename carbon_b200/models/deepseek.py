@@ -241,9 +241,12 @@ class DeepseekModel:
         window = torch.where(p[:, None] - back[None, :] >= 0, toks, -1)
         rows = R.engram_hash_ids(window, cfg.engram_orders, cfg.engram_heads, cfg.engram_primes, cfg.vocab_size)
         T = X.shape[0]
+        img = cfg.image_token_id
         if not self.on_gpu:
             kv = E.wkv(E.table[rows].reshape(T, -1))
             Xn = R.engram_gate(X, kv, E.qw, E.kw, cfg.rms_eps, cfg.engram_clamp).to(X.dtype)
+            if img >= 0:
+                Xn = torch.where((self._tok_local.long() == img)[:, None, None], X, Xn)
             return Xn, (None if sumsq is None else Xn.float().pow(2).sum((1, 2)))
         from ..ops._ext import ext
 
@@ -252,7 +255,8 @@ class DeepseekModel:
         kv = E.wkv(emb).contiguous()
         X = X.contiguous()
         ss = torch.empty(T, dtype=torch.float32, device=dev)
-        ext().engram_gate(X, kv, E.qw, E.kw, cfg.rms_eps, cfg.engram_clamp, ss)
+        ext().engram_gate(X, kv, E.qw, E.kw, cfg.rms_eps, cfg.engram_clamp, ss,
+                          self._tok_local.to(torch.int32).contiguous() if img >= 0 else None, img)
         return X, ss
 
     def _load_layer(self, i: int, get) -> Layer:
@@ -319,6 +323,7 @@ class DeepseekModel:
             e0 = pc.ep_rank * El
             L.gate = Lin(get(f + "gate.weight"), dev, fp8=False)
             L.gate_b = get(f + "gate.bias")
+            L.gate_b_img = get(f + "gate.bias_img").float().contiguous() if cfg.image_token_id >= 0 else None
             if dev.type == "cpu":
                 L.e_w1 = get(f + "experts.w1", slice(e0, e0 + El))
                 L.e_w3 = get(f + "experts.w3", slice(e0, e0 + El))
@@ -647,7 +652,9 @@ class DeepseekModel:
         with region("moe.router"):
             logits = L.gate(h, out_dtype=torch.float32)
             w, ids = C.router_topk(logits, L.gate_b, cfg.n_activated_experts, cfg.score_func, cfg.route_scale,
-                                   cfg.norm_topk_prob)
+                                   cfg.norm_topk_prob, bias_img=L.gate_b_img,
+                                   tok=self._tok_local if L.gate_b_img is not None else None,
+                                   img_id=cfg.image_token_id)
         self._tr(f"{i}.router_ids", ids)
         shared = None
         if L.shared is not None:
@@ -714,6 +721,8 @@ class DeepseekModel:
         T_all = fb.ids.shape[0]
         self.pctx.set_bounds(fb.bounds if fb.bounds is not None else [0, T_all])
         self._dsa = {}                 # DSA selections of this forward's index-source layers
+        lo, hi = self.pctx.local
+        self._tok_local = fb.ids[lo:hi]    # this rank's token ids (multimodal router bias, Engram image skip)
         with region("embed"):
             X, sumsq = self.embed_tokens(fb.ids)
         if cfg.engram_layers:

@@ -58,13 +58,20 @@ def rope_(x: torch.Tensor, off: int, dim: int, table: torch.Tensor, pos: torch.T
 
 
 def router_topk(logits: torch.Tensor, bias: Optional[torch.Tensor], k: int, score_func: str, route_scale: float,
-                norm: bool) -> Tuple[torch.Tensor, torch.Tensor]:
+                norm: bool, bias_img: Optional[torch.Tensor] = None, tok: Optional[torch.Tensor] = None,
+                img_id: int = -1) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Biased top-k router; with ``bias_img``, tokens whose id (``tok``) is ``img_id`` rank with that bias."""
     if not logits.is_cuda:
+        if bias_img is not None and tok is not None:
+            is_img = (tok.long() == img_id)[:, None]
+            b = bias if bias is not None else torch.zeros_like(bias_img)
+            bias = torch.where(is_img, bias_img.float()[None, :], b.float()[None, :])
         return R.router_topk(logits, bias, k, score_func, route_scale, norm)
     T = logits.shape[0]
     w = torch.empty(T, k, dtype=torch.float32, device=logits.device)
     ids = torch.empty(T, k, dtype=torch.int32, device=logits.device)
-    ext().router_topk(logits.float().contiguous(), bias, k, SCORE_FUNCS[score_func], norm, float(route_scale), w, ids)
+    ext().router_topk(logits.float().contiguous(), bias, k, SCORE_FUNCS[score_func], norm, float(route_scale), w, ids,
+                      bias_img, tok.to(torch.int32).contiguous() if tok is not None else None, int(img_id))
     return w, ids
 
 

@@ -74,6 +74,8 @@ def param_shapes(cfg: ModelConfig) -> "OrderedDict[str, Tuple[Tuple[int, ...], s
             E, I = cfg.n_routed_experts, cfg.moe_intermediate
             p[L + "ffn.gate.weight"] = ((E, D), "normal")
             p[L + "ffn.gate.bias"] = ((E,), "normal")
+            if cfg.image_token_id >= 0:
+                p[L + "ffn.gate.bias_img"] = ((E,), "normal")
             p[L + "ffn.experts.w1"] = ((E, I, D), "normal")
             p[L + "ffn.experts.w3"] = ((E, I, D), "normal")
             p[L + "ffn.experts.w2"] = ((E, D, I), "normal")
@@ -216,7 +218,11 @@ class RefModel:
         if not cfg.is_moe_layer(i):
             return ops.swiglu(h @ w[L + "w1"].t(), h @ w[L + "w3"].t(), cfg.swiglu_limit) @ w[L + "w2"].t()
         logits = h @ w[L + "gate.weight"].t()
-        wts, ids = ops.router_topk(logits, w[L + "gate.bias"], cfg.n_activated_experts, cfg.score_func,
+        bias = w[L + "gate.bias"]
+        if cfg.image_token_id >= 0:             # image tokens rank with their own bias
+            is_img = (self._ids.long() == cfg.image_token_id)[:, None]
+            bias = torch.where(is_img, w[L + "gate.bias_img"][None, :], bias[None, :])
+        wts, ids = ops.router_topk(logits, bias, cfg.n_activated_experts, cfg.score_func,
                                    cfg.route_scale, cfg.norm_topk_prob)
         if self.forced_routing is not None and i in self.forced_routing:
             ids = self.forced_routing[i].to(ids.dtype)
@@ -253,6 +259,7 @@ class RefModel:
         T = ids.shape[0]
         pos = torch.arange(T) if pos is None else pos
         self._dsa = {}
+        self._ids = ids
         X = w["embed.weight"][ids.long()][:, None, :].expand(T, cfg.hc_mult, cfg.hidden_size).clone()
         for i in range(cfg.n_layers):
             L = f"layers.{i}."
@@ -274,7 +281,10 @@ class RefModel:
         rows = ops.engram_hash_ids(window, cfg.engram_orders, cfg.engram_heads, cfg.engram_primes, cfg.vocab_size)
         emb = w[L + "table"][rows].reshape(T, -1)                                  # [T, cols * dim]
         kv = emb @ w[L + "wkv.weight"].t()
-        return ops.engram_gate(X, kv, w[L + "q_weight"], w[L + "k_weight"], cfg.rms_eps, cfg.engram_clamp)
+        Xn = ops.engram_gate(X, kv, w[L + "q_weight"], w[L + "k_weight"], cfg.rms_eps, cfg.engram_clamp)
+        if cfg.image_token_id >= 0:             # image tokens take no n-gram memory update
+            Xn = torch.where((ids.long() == cfg.image_token_id)[:, None, None], X, Xn)
+        return Xn
 
     def head(self, X: torch.Tensor) -> torch.Tensor:
         cfg, w = self.cfg, self.w

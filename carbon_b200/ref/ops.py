@@ -237,7 +237,10 @@ def router_topk(logits: torch.Tensor, bias: Optional[torch.Tensor], k: int, scor
         act = torch.softmax(lf, dim=-1)
     else:
         raise ValueError(score_func)
-    key = act + bias.float()[None, :] if bias is not None else act.clone()
+    if bias is None:
+        key = act.clone()
+    else:                                   # [E] shared, or [T, E] per token (multimodal bias switch)
+        key = act + (bias.float()[None, :] if bias.dim() == 1 else bias.float())
     T, E = key.shape
     if n_groups > 1:
         g = key.view(T, n_groups, E // n_groups)

@@ -201,6 +201,6 @@ def test_engram_kernels_vs_oracle():
     ref = R.engram_gate(X.float(), kv.float(), qw, kw, 1e-6, 10.0)
     Xg = X.cuda().contiguous()
     ss = torch.empty(T, device="cuda")
-    ext().engram_gate(Xg, kv.cuda(), qw.cuda(), kw.cuda(), 1e-6, 10.0, ss)
+    ext().engram_gate(Xg, kv.cuda(), qw.cuda(), kw.cuda(), 1e-6, 10.0, ss, None, -1)
     assert _rel(Xg.cpu(), ref) < 1e-2
     assert _rel(ss.cpu(), Xg.float().pow(2).sum((1, 2)).cpu()) < 1e-4
