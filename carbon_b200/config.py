@@ -44,6 +44,9 @@ class ModelConfig:
     # layer reuses the selection of the most recent source layer; layers before the first source attend densely.
     # Empty: every layer runs its own indexer.
     index_sources: tuple = ()
+    # indexer q and k in MXFP4 (e2m1 + UE8M0 per 32 dims; the reference's 68-byte index keys,
+    # dec/cuda_paged_logits.py:35-37): both are rounded to fp4 values before the logits
+    index_fp4: bool = False
     # per-head learned attention sink: one extra logit in each softmax denominator (attn.sink [n_heads] fp32)
     attn_sink: bool = False
     # attention kind.  "mla": q/k = [nope | RoPE] per head, keys and values up-projected from the kv latent (wkv_b);
@@ -234,7 +237,7 @@ def tiny_v4_config() -> ModelConfig:
     grouped low-rank output projection, sliding window 16, per-head sinks, DSA index sources, sqrt-softplus router."""
     return tiny_config().replace(attn_kind="latent_mqa", o_groups=2, o_lora_rank=64, swa_window=16, attn_sink=True,
                                  index_sources=(0,), index_topk=16, score_func="sqrtsoftplus", engram_layers=(1,),
-                                 engram_heads=2, engram_dim=64, engram_rows=97)
+                                 engram_heads=2, engram_dim=64, engram_rows=97, index_fp4=True)
 
 
 def deepseek_v4_config() -> ModelConfig:
@@ -248,6 +251,7 @@ def deepseek_v4_config() -> ModelConfig:
         n_heads=64, q_lora_rank=1280, kv_lora_rank=512, qk_nope_head_dim=448, qk_rope_head_dim=64, v_head_dim=512,
         max_position=65536, index_n_heads=32, index_head_dim=128, index_topk=512, index_sources=(2, 8, 14),
         attn_sink=True, attn_kind="latent_mqa", o_groups=8, o_lora_rank=1024, swa_window=128, engram_layers=(1, 14),
+        index_fp4=True,
         engram_orders=(2, 3), engram_heads=12, engram_dim=256, engram_rows=1 << 20,
         n_routed_experts=384, n_activated_experts=6, n_shared_experts=1, moe_intermediate=2304,
         score_func="sqrtsoftplus", route_scale=2.5,

@@ -479,6 +479,9 @@ class DeepseekModel:
         k = k.view(T, 1, Di)
         C.rope_(k, 0, dr, self.cos_sin, pos)
         w = (L.idx_wp(h, out_dtype=torch.float32) * (Hi ** -0.5) * (Di ** -0.5)).float()
+        if cfg.index_fp4:               # fp4 values are exact in bf16: the bf16 logits kernels compute fp4 products
+            q = R.fake_quant_mxfp4(q)
+            k = R.fake_quant_mxfp4(k)
         return q, k.view(T, Di), w
 
     def _prefill_key_masks(self, idx_l, fb: ForwardBatch, gather: bool = True):

@@ -210,6 +210,8 @@ class RefModel:
         k = ops.layer_norm(h @ w[L + "wk.weight"].t(), w[L + "k_norm.weight"], w[L + "k_norm.bias"], 1e-6)
         k = torch.cat([ops.apply_rope(k[:, None, :dr], pos, cfg.rope_theta)[:, 0], k[:, dr:]], dim=-1)
         wt = (h @ w[L + "weights_proj.weight"].t()) * (Hi ** -0.5) * (Di ** -0.5)
+        if cfg.index_fp4:
+            q, k = ops.fake_quant_mxfp4(q), ops.fake_quant_mxfp4(k)
         return q, k, wt
 
     def ffn(self, i: int, h: torch.Tensor) -> torch.Tensor:

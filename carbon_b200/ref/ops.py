@@ -171,6 +171,22 @@ def dequant_fp8_rows32(q: torch.Tensor, sf: torch.Tensor) -> torch.Tensor:
     return q.float() * torch.pow(2.0, sf.float() - 127.0).repeat_interleave(32, dim=1)
 
 
+def fake_quant_mxfp4(x: torch.Tensor, block: int = 32) -> torch.Tensor:
+    """Round x (any shape, last dim a multiple of 32) to MXFP4 values in its own dtype: per 32-element block the
+    scale of ``quant_mxfp4`` and the nearest e2m1 value, ties to the smaller magnitude (identical to
+    dequant_mxfp4(quant_mxfp4(x))).  Arithmetic only, so it runs on any device without large temporaries."""
+    shp = x.shape
+    xb = x.float().reshape(-1, shp[-1] // block, block)
+    amax = xb.abs().amax(-1, keepdim=True)
+    m, ex = torch.frexp(amax / 6.0)
+    e = torch.where(amax > 0, ex - (m == 0.5).to(ex.dtype), torch.zeros_like(ex)).clamp(-127, 127)
+    sc = torch.pow(2.0, e.float())
+    mag = xb.abs() / sc
+    step = torch.where(mag < 2.0, 0.5, torch.where(mag < 4.0, 1.0, 2.0))
+    r = (torch.ceil(mag / step - 0.5) * step).clamp(max=6.0)
+    return (torch.sign(xb) * r * sc).reshape(shp).to(x.dtype)
+
+
 def fp8_gemm(a_q, a_s, b_q, b_s) -> torch.Tensor:
     """Block-scaled fp8 GEMM oracle: dequantise both operands and multiply in fp32. Returns [M, N] fp32."""
     return dequant_fp8_rows(a_q, a_s) @ dequant_fp8_blocks(b_q, b_s).t()

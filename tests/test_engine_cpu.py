@@ -45,3 +45,14 @@ def test_tiny_engine_matches_oracle(variant):
             err = (got - exp).abs().max().item()
             assert err < 1e-4, (b, step, err)
     assert eng.cache.alloc.num_free() == 16 - 1   # all request pages returned (page 0 is the scratch page)
+
+
+def test_fake_quant_mxfp4_matches_codec():
+    """The indexer's arithmetic fp4 rounding equals the MXFP4 encode/decode pair (scales, ties, signs, zeros)."""
+    from carbon_b200.ref import ops as R
+
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(64, 128, generator=g) * torch.logspace(-3, 3, 64)[:, None]
+    x[0, :32] = 0.0
+    x[1, :8] = torch.tensor([0.25, 1.75, 2.5, 3.5, 5.0, 6.0, -0.75, -5.0])
+    assert torch.equal(R.fake_quant_mxfp4(x), R.dequant_mxfp4(*R.quant_mxfp4(x)))
