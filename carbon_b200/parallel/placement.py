@@ -75,3 +75,72 @@ def apply(model, layer: int, perm: torch.Tensor) -> None:
         L.e_w1 = L.e_w1[p].contiguous()
         L.e_w3 = L.e_w3[p].contiguous()
         L.e_w2 = L.e_w2[p].contiguous()
+
+
+def _exchange_experts(t: torch.Tensor, perm: torch.Tensor, E: int, ep: int, rank: int, group) -> torch.Tensor:
+    """t: this rank's experts stacked on dim 0 ([El * rows, ...], old labels).  Returns the rows of the experts this
+    rank owns under ``perm`` (new labels [rank*El, (rank+1)*El), in order), fetched with one all-to-all."""
+    import torch.distributed as dist
+
+    El = E // ep
+    rows = t.shape[0] // El
+    p = perm.tolist()
+    send_idx, send_counts = [], []
+    for d in range(ep):                      # experts destination d needs from this rank, in new-id order
+        mine = [p[n] - rank * El for n in range(d * El, (d + 1) * El) if p[n] // El == rank]
+        send_idx += mine
+        send_counts.append(len(mine) * rows)
+    recv_src = [p[n] // El for n in range(rank * El, (rank + 1) * El)]
+    recv_counts = [sum(1 for s in recv_src if s == r) * rows for r in range(ep)]
+    tv = t.view(torch.uint8) if t.dtype == torch.float8_e4m3fn else t      # NCCL moves fp8 as bytes
+    tv = tv.view(El, rows, *tv.shape[1:])
+    send = tv[torch.tensor(send_idx, dtype=torch.long, device=t.device)].reshape(-1, *tv.shape[2:]).contiguous() \
+        if send_idx else tv.new_empty((0,) + tuple(tv.shape[2:]))
+    recv = tv.new_empty((sum(recv_counts),) + tuple(tv.shape[2:]))
+    dist.all_to_all_single(recv, send, recv_counts, send_counts, group=group)
+    # received blocks arrive grouped by source rank, each group in new-id order
+    starts, off = [], 0
+    for r in range(ep):
+        starts.append(off)
+        off += recv_counts[r]
+    seen = [0] * ep
+    parts = []
+    for s in recv_src:
+        parts.append(recv[starts[s] + seen[s] * rows: starts[s] + (seen[s] + 1) * rows])
+        seen[s] += 1
+    out = torch.cat(parts) if parts else recv
+    return out.view(torch.float8_e4m3fn) if t.dtype == torch.float8_e4m3fn else out
+
+
+def redistribute(model, layer: int, perm: torch.Tensor) -> None:
+    """Relabel the experts of one MoE layer across the EP ranks (``perm[new] = old``): every rank permutes its
+    replicated router rows and bias, and the stacked expert weights move to their new owners with one all-to-all
+    per tensor (the reference moves per-expert tensors with one NCCL all_to_all, ``placement.py:89-128``).  All
+    ranks call it with the same perm, in the same order."""
+    L = model.layers[layer]
+    pc = model.pctx
+    E, ep = perm.numel(), pc.ep
+    if ep == 1:
+        return apply(model, layer, perm)
+    assert L.moe
+    group = getattr(pc, "group", None)
+    p = perm.to(L.gate_b.device)
+    if L.gate.kind == "f32" or L.gate.kind == "bf16":
+        L.gate.w[:E] = L.gate.w[:E][p.to(L.gate.w.device)]
+    L.gate_b.copy_(L.gate_b[p])
+    if getattr(L, "gate_b_img", None) is not None:
+        L.gate_b_img.copy_(L.gate_b_img[p.to(L.gate_b_img.device)])
+    rank = pc.ep_rank
+    if model.on_gpu:
+        from ..ops.quant import Fp8Weight, pack_sf
+
+        for name in ("e_w13", "e_w2"):
+            W = getattr(L, name)
+            q = _exchange_experts(W.q, perm, E, ep, rank, group)
+            scale = _exchange_experts(W.scale.contiguous(), perm, E, ep, rank, group)
+            setattr(L, name, Fp8Weight(q.contiguous(), pack_sf(scale.repeat_interleave(128, dim=0)[: q.shape[0]]),
+                                       scale))
+    else:
+        L.e_w1 = _exchange_experts(L.e_w1.contiguous(), perm, E, ep, rank, group)
+        L.e_w3 = _exchange_experts(L.e_w3.contiguous(), perm, E, ep, rank, group)
+        L.e_w2 = _exchange_experts(L.e_w2.contiguous(), perm, E, ep, rank, group)

@@ -31,3 +31,55 @@ def test_relabel_is_output_preserving():
     assert out == ref
     for a, b in zip(h, h_ref):
         assert (a - b).abs().max() < 1e-4
+
+
+def _redistribute_worker(rank, world, port, q):
+    import os
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from carbon_b200.parallel.dist import DistCtx
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    try:
+        cfg = tiny_config()
+        w = init_weights(cfg, seed=0)
+        e = Engine(cfg, "cpu", source=WeightSource(cfg, state=w), num_pages=16, page_size=16,
+                   pctx=DistCtx(rank, world))
+        prompts = [torch.arange(40).tolist(), (torch.arange(30) * 7 % cfg.vocab_size).tolist()]
+        ref, h_ref = e.generate(prompts, 5, return_logits=True)
+        for layer in range(cfg.n_layers):
+            perm = torch.randperm(cfg.n_routed_experts, generator=torch.Generator().manual_seed(10 + layer))
+            placement.redistribute(e.model, layer, perm)
+        out, h = e.generate(prompts, 5, return_logits=True)
+        err = max(float((a - b).abs().max()) for a, b in zip(h, h_ref))
+        q.put((rank, out == ref, err))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_redistribute_across_ranks_is_output_preserving():
+    """EP=2 over gloo: a random relabel per layer moves expert weights between the ranks (all-to-all) and the
+    served outputs stay the same."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_redistribute_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(2)]
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, same, err in res:
+        assert same and err < 1e-4, (rank, same, err)
