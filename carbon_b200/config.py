@@ -80,6 +80,13 @@ class ModelConfig:
     # (ffn.gate.bias_img) and take no Engram update (cuda_moe_front.py:265-269, dspd_w22/dspd/engram.py:261).
     # -1: text only.
     image_token_id: int = -1
+    # bounded replay of the late layers (the reference's "decoder SWA bounded replay": layers >= 20 of a prefill run
+    # only each request's last <= 128 tokens; rehome_block.py:195-197, dspd_w22/dspd/mlp.py:15-18).  Layers from
+    # late_layer_start on are window-only (no DSA selection).  A prefill keeps only each request's last late_replay
+    # tokens from that layer on; keys older than that tail never exist at the late layers, for the request's later
+    # decode steps too.  -1: off.
+    late_layer_start: int = -1
+    late_replay: int = 128
     # MoE
     n_routed_experts: int = 256
     n_activated_experts: int = 8
@@ -126,9 +133,12 @@ class ModelConfig:
     def use_indexer(self) -> bool:
         return self.index_n_heads > 0 and self.index_topk > 0
 
+    def is_late_layer(self, layer: int) -> bool:
+        return 0 <= self.late_layer_start <= layer
+
     def index_source(self, layer: int) -> Optional[int]:
-        """Layer whose DSA selection this layer's attention uses (None: dense attention)."""
-        if not self.use_indexer:
+        """Layer whose DSA selection this layer's attention uses (None: dense or window-only attention)."""
+        if not self.use_indexer or self.is_late_layer(layer):
             return None
         if not self.index_sources:
             return layer
@@ -137,6 +147,8 @@ class ModelConfig:
 
     def has_indexer(self, layer: int) -> bool:
         """Whether this layer holds indexer weights and writes indexer keys to the cache."""
+        if self.is_late_layer(layer):
+            return False
         return self.use_indexer and (not self.index_sources or layer in self.index_sources)
 
     def is_moe_layer(self, layer: int) -> bool:
@@ -201,6 +213,10 @@ class ModelConfig:
         assert self.swa_window >= 0
         if self.engram_layers:
             assert self.engram_dim % 32 == 0 and self.engram_cols > 0 and min(self.engram_orders) >= 1
+        if self.late_layer_start >= 0:
+            assert self.attn_kind == "latent_mqa" and 0 < self.swa_window <= self.late_replay, \
+                "bounded late-layer replay needs window-only latent-MQA late layers with swa_window <= late_replay"
+            assert all(l < self.late_layer_start for l in self.engram_layers), "Engram layers precede the late layers"
 
 
 def tiny_config() -> ModelConfig:
@@ -251,7 +267,7 @@ def deepseek_v4_config() -> ModelConfig:
         n_heads=64, q_lora_rank=1280, kv_lora_rank=512, qk_nope_head_dim=448, qk_rope_head_dim=64, v_head_dim=512,
         max_position=65536, index_n_heads=32, index_head_dim=128, index_topk=512, index_sources=(2, 8, 14),
         attn_sink=True, attn_kind="latent_mqa", o_groups=8, o_lora_rank=1024, swa_window=128, engram_layers=(1, 14),
-        index_fp4=True,
+        index_fp4=True, late_layer_start=20, late_replay=128,
         engram_orders=(2, 3), engram_heads=12, engram_dim=256, engram_rows=1 << 20,
         n_routed_experts=384, n_activated_experts=6, n_shared_experts=1, moe_intermediate=2304,
         score_func="sqrtsoftplus", route_scale=2.5,

@@ -34,6 +34,7 @@ class Request:
     pages: List[int] = field(default_factory=list)
     n_cached: int = 0            # tokens whose KV is in the cache
     done: bool = False
+    late_from: int = 0           # first position that exists at the late layers (bounded late-layer replay)
 
     @property
     def seq_len(self) -> int:
@@ -127,6 +128,9 @@ class Engine:
             ids += toks
             starts.append(r.n_cached)
             lens.append(len(toks))
+        if self.cfg.late_layer_start >= 0:
+            for r, n in zip(reqs, lens):
+                r.late_from = max(0, n - self.cfg.late_replay)
         out_loc, pos = prefill_metadata([r.pages for r in reqs], starts, lens, self.page_size)
         cu = [0]
         for n in lens:
@@ -153,13 +157,16 @@ class Engine:
                                                           self.page_size, bucket)
         ids = torch.zeros(bucket, dtype=torch.int32)
         ids[:B] = torch.tensor([r.out[-1] for r in reqs], dtype=torch.int32)
+        late = torch.zeros(bucket, dtype=torch.int32)
+        late[:B] = torch.tensor([r.late_from for r in reqs], dtype=torch.int32)
         if self.cuda_graphs and bucket is not None:
             g = self._graph(bucket, key_slots.shape[1])
-            logits = g.run(ids, pos, out_loc, key_slots, n_keys)[:B]
+            logits = g.run(ids, pos, out_loc, key_slots, n_keys, late)[:B]
         else:
             dev = self.device
             fb = ForwardBatch(ids=ids.to(dev), pos=pos.to(dev), out_loc=out_loc.to(dev), is_prefill=False,
-                              key_slots=key_slots.to(dev), n_keys=n_keys.to(dev), bounds=self._bounds([1] * bucket))
+                              key_slots=key_slots.to(dev), n_keys=n_keys.to(dev), bounds=self._bounds([1] * bucket),
+                              late_from=late.to(dev))
             logits = self.model.forward(fb, self.cache)[:B]
         for r in reqs:
             r.n_cached = r.seq_len
@@ -173,7 +180,7 @@ class Engine:
         attending to the cache plus the rows before it. Greedy acceptance keeps the longest draft prefix the target
         agrees with and adds the target's next token. Returns the accepted new tokens per request (>= 1 each).
         KV rows of rejected drafts are simply overwritten later (positions are slot-addressed)."""
-        rows_pt, rows_len, ids = [], [], []
+        rows_pt, rows_len, ids, late = [], [], [], []
         for r, t, d in zip(reqs, last_tokens, drafts):
             base = r.seq_len
             seq = [int(t)] + [int(x) for x in d]
@@ -182,12 +189,13 @@ class Engine:
                 rows_pt.append(r.pages)
                 rows_len.append(base + j + 1)
                 ids.append(tok)
+                late.append(r.late_from)
         n = len(ids)
         out_loc, key_slots, n_keys, pos = decode_metadata(rows_pt, rows_len, self.page_size, n)
         dev = self.device
         fb = ForwardBatch(ids=torch.tensor(ids, dtype=torch.int32).to(dev), pos=pos.to(dev), out_loc=out_loc.to(dev),
                           is_prefill=False, key_slots=key_slots.to(dev), n_keys=n_keys.to(dev),
-                          bounds=self._bounds([1] * n))
+                          bounds=self._bounds([1] * n), late_from=torch.tensor(late, dtype=torch.int32).to(dev))
         logits = self.model.forward(fb, self.cache)
         pred = torch.argmax(logits.float(), dim=-1).tolist()
         accepted, i = [], 0
@@ -282,8 +290,10 @@ class _DecodeGraph:
         self.key_slots = torch.full((bucket, lmax), -1, dtype=torch.int32, device=dev)
         self.key_slots[:, 0] = 0
         self.n_keys = torch.ones(bucket, dtype=torch.int32, device=dev)
+        self.late_from = torch.zeros(bucket, dtype=torch.int32, device=dev)
         fb = ForwardBatch(ids=self.ids, pos=self.pos, out_loc=self.out_loc, is_prefill=False,
-                          key_slots=self.key_slots, n_keys=self.n_keys, bounds=eng._bounds([1] * bucket))
+                          key_slots=self.key_slots, n_keys=self.n_keys, bounds=eng._bounds([1] * bucket),
+                          late_from=self.late_from)
         s = torch.cuda.Stream()
         s.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(s):
@@ -294,8 +304,10 @@ class _DecodeGraph:
         with torch.cuda.graph(self.graph):
             self.logits = eng.model.forward(fb, eng.cache)
 
-    def run(self, ids, pos, out_loc, key_slots, n_keys) -> torch.Tensor:
+    def run(self, ids, pos, out_loc, key_slots, n_keys, late_from=None) -> torch.Tensor:
         self.ids.copy_(ids, non_blocking=True)
+        if late_from is not None:
+            self.late_from.copy_(late_from, non_blocking=True)
         self.pos.copy_(pos, non_blocking=True)
         self.out_loc.copy_(out_loc, non_blocking=True)
         L = key_slots.shape[1]

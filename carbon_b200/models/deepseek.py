@@ -116,6 +116,7 @@ class ForwardBatch:
     n_keys: Optional[torch.Tensor] = None     # decode: [B] int32
     logits_rows: Optional[torch.Tensor] = None  # rows that need logits (default: all)
     bounds: Optional[List[int]] = None          # per-rank token shard bounds (multi-rank; sequence-aligned)
+    late_from: Optional[torch.Tensor] = None    # decode: [B] first position that exists at the late layers
 
 
 class Layer:
@@ -532,7 +533,8 @@ class DeepseekModel:
             lens = [b - a for a, b in zip(cu[:-1], cu[1:])]
             start = torch.repeat_interleave(torch.tensor(cu[:-1], dtype=torch.long),
                                             torch.tensor(lens, dtype=torch.long)).to(dev)[rows]
-            nk = fb.pos[rows].long() + 1
+            # keys: the sequence's batch tokens up to the query (a bounded-replay tail starts after position 0)
+            nk = fb.pos[rows].long() - fb.pos[start].long() + 1
             Lmax = max(lens) if lens else 1
             j = torch.arange(Lmax, device=dev)
             src_i = (start[:, None] + j[None, :]).clamp(max=fb.out_loc.shape[0] - 1)
@@ -564,7 +566,10 @@ class DeepseekModel:
             parts.append(sel)
         if W > 0:
             wj = nk[:, None] - W + torch.arange(W, device=dev)[None, :]
-            win = torch.where(wj >= 0, ks.gather(1, wj.clamp(min=0)).long(), -1).to(torch.int32)
+            lowest = 0
+            if not fb.is_prefill and fb.late_from is not None and cfg.is_late_layer(i):
+                lowest = fb.late_from[rows].long()[:, None]      # keys before the replayed tail do not exist here
+            win = torch.where(wj >= lowest, ks.gather(1, wj.clamp(min=0)).long(), -1).to(torch.int32)
             parts.append(win)
         elif src is None:
             parts.append(ks)                        # dense causal
@@ -577,7 +582,7 @@ class DeepseekModel:
         dev = fb.pos.device
         start = torch.repeat_interleave(torch.tensor(cu[:-1], dtype=torch.long),
                                         torch.tensor(lens, dtype=torch.long)).to(dev)[lo:hi]
-        nk = fb.pos[lo:hi].long() + 1
+        nk = fb.pos[lo:hi].long() - fb.pos[start].long() + 1
         j = torch.arange(max(lens) if lens else 1, device=dev)
         src_i = (start[:, None] + j[None, :]).clamp(max=fb.out_loc.shape[0] - 1)
         return torch.where(j[None, :] < nk[:, None], fb.out_loc[src_i].long(), -1).to(torch.int32)
@@ -732,6 +737,9 @@ class DeepseekModel:
             cache.write_tokens(fb.out_loc, fb.ids)
         for i in range(cfg.n_layers):
             L = self.layers[i]
+            if i == cfg.late_layer_start and fb.is_prefill:
+                with region("late.enter_tail"):
+                    fb, X, sumsq = self._enter_tail(fb, X, sumsq)
             if L.engram is not None:
                 with region("engram"):
                     X, sumsq = self.engram(i, X, sumsq, fb, cache)
@@ -755,6 +763,32 @@ class DeepseekModel:
             self._tr(f"{i}.X_ffn", X)
         with region("head"):
             return self.logits(X, sumsq, fb)
+
+    def _enter_tail(self, fb: ForwardBatch, X, sumsq):
+        """Bounded late-layer replay: from here on a prefill keeps only each sequence's last late_replay tokens.
+        Returns the tail batch (same sequences, fewer tokens; shard bounds recomputed, still sequence-aligned) and
+        this rank's rows of X / sumsq for it."""
+        cfg, pc = self.cfg, self.pctx
+        cu, R_ = fb.cu_seqlens, cfg.late_replay
+        old_bounds = fb.bounds if fb.bounds is not None else [0, cu[-1]]
+        keep, tail_cu = [], [0]
+        for a, e in zip(cu[:-1], cu[1:]):
+            s0 = max(a, e - R_)
+            keep += range(s0, e)
+            tail_cu.append(tail_cu[-1] + e - s0)
+        bounds = [sum(1 for k in keep if k < b) for b in old_bounds]
+        lo = old_bounds[pc.rank] if len(old_bounds) > 2 else 0
+        hi = old_bounds[pc.rank + 1] if len(old_bounds) > 2 else old_bounds[-1]
+        dev = X.device
+        keep_t = torch.tensor(keep, dtype=torch.long).to(dev)
+        local = torch.tensor([k - lo for k in keep if lo <= k < hi], dtype=torch.long).to(dev)
+        rows = torch.tensor([c - 1 for c in tail_cu[1:]], dtype=torch.int32).to(dev)
+        tb = ForwardBatch(ids=fb.ids[keep_t], pos=fb.pos[keep_t], out_loc=fb.out_loc[keep_t], is_prefill=True,
+                          cu_seqlens=tail_cu, logits_rows=rows, bounds=bounds)
+        pc.set_bounds(bounds)
+        lo2, hi2 = pc.local
+        self._tok_local = tb.ids[lo2:hi2]
+        return tb, X[local].contiguous(), (sumsq[local].contiguous() if sumsq is not None else None)
 
     def _tr(self, name, t):
         if self.trace is not None:

@@ -256,7 +256,9 @@ class RefModel:
         return ops.mhc_post_mix(X, fn_apply(y), post, comb)
 
     # -- whole model -----------------------------------------------------------------------------------------------
-    def forward(self, ids: torch.Tensor, pos: torch.Tensor = None) -> torch.Tensor:
+    def forward(self, ids: torch.Tensor, pos: torch.Tensor = None, late_from: int = None) -> torch.Tensor:
+        """late_from: first position that exists at the late layers (bounded replay; default: the prompt's last
+        late_replay tokens).  Returns logits of the tokens that reach the head."""
         cfg, w = self.cfg, self.w
         T = ids.shape[0]
         pos = torch.arange(T) if pos is None else pos
@@ -264,6 +266,11 @@ class RefModel:
         self._ids = ids
         X = w["embed.weight"][ids.long()][:, None, :].expand(T, cfg.hc_mult, cfg.hidden_size).clone()
         for i in range(cfg.n_layers):
+            if i == cfg.late_layer_start:
+                lf = max(0, T - cfg.late_replay) if late_from is None else late_from
+                keep = pos >= lf
+                X, pos, ids = X[keep], pos[keep], ids[keep]
+                self._ids = ids
             L = f"layers.{i}."
             if i in cfg.engram_layers:
                 X = self.engram(i, X, ids, pos)
@@ -298,8 +305,9 @@ class RefModel:
         """Recompute-everything greedy decode. Returns (new token ids, last-position logits of every step)."""
         ids = prompt.clone()
         toks, logits = [], []
+        late_from = max(0, prompt.shape[0] - self.cfg.late_replay)     # fixed by the prompt (bounded replay)
         for _ in range(n_new + 1):
-            lg = self.forward(ids)[-1]
+            lg = self.forward(ids, late_from=late_from)[-1]
             logits.append(lg)
             if len(toks) == n_new:
                 break
