@@ -191,12 +191,23 @@ class Engine:
                 ids.append(tok)
                 late.append(r.late_from)
         n = len(ids)
-        out_loc, key_slots, n_keys, pos = decode_metadata(rows_pt, rows_len, self.page_size, n)
+        # verify rows are decode rows (one token each, its own key list): a captured decode graph of a large enough
+        # bucket serves them (the reference captures verify buckets of 6-row multiples)
+        bucket = self._bucket(n) if self.cuda_graphs else None
+        out_loc, key_slots, n_keys, pos = decode_metadata(rows_pt, rows_len, self.page_size, bucket or n)
         dev = self.device
-        fb = ForwardBatch(ids=torch.tensor(ids, dtype=torch.int32).to(dev), pos=pos.to(dev), out_loc=out_loc.to(dev),
-                          is_prefill=False, key_slots=key_slots.to(dev), n_keys=n_keys.to(dev),
-                          bounds=self._bounds([1] * n), late_from=torch.tensor(late, dtype=torch.int32).to(dev))
-        logits = self.model.forward(fb, self.cache)
+        if bucket is not None:
+            ids_t = torch.zeros(bucket, dtype=torch.int32)
+            ids_t[:n] = torch.tensor(ids, dtype=torch.int32)
+            late_t = torch.zeros(bucket, dtype=torch.int32)
+            late_t[:n] = torch.tensor(late, dtype=torch.int32)
+            logits = self._graph(bucket, key_slots.shape[1]).run(ids_t, pos, out_loc, key_slots, n_keys, late_t)[:n]
+        else:
+            fb = ForwardBatch(ids=torch.tensor(ids, dtype=torch.int32).to(dev), pos=pos.to(dev),
+                              out_loc=out_loc.to(dev), is_prefill=False, key_slots=key_slots.to(dev),
+                              n_keys=n_keys.to(dev), bounds=self._bounds([1] * n),
+                              late_from=torch.tensor(late, dtype=torch.int32).to(dev))
+            logits = self.model.forward(fb, self.cache)
         pred = torch.argmax(logits.float(), dim=-1).tolist()
         accepted, i = [], 0
         for r, t, d in zip(reqs, last_tokens, drafts):

@@ -204,3 +204,21 @@ def test_engram_kernels_vs_oracle():
     ext().engram_gate(Xg, kv.cuda(), qw.cuda(), kw.cuda(), 1e-6, 10.0, ss, None, -1)
     assert _rel(Xg.cpu(), ref) < 1e-2
     assert _rel(ss.cpu(), Xg.float().pow(2).sum((1, 2)).cpu()) < 1e-4
+
+
+def test_speculative_verify_in_decode_graph():
+    """Target-verify rows replayed through a captured decode graph give the same accepted tokens as eager verify."""
+    from carbon_b200.engine.spec import NgramDrafter
+
+    cfg = small_gpu_config().replace(n_layers=2)
+    src = WeightSource(cfg, seed=5)
+    g = torch.Generator().manual_seed(4)
+    base = torch.randint(0, cfg.vocab_size, (30,), generator=g).tolist()
+    prompts = [base * 3, torch.randint(0, cfg.vocab_size, (50,), generator=g).tolist()]
+    e1 = Engine(cfg, device="cuda", source=src, num_pages=32, page_size=64, cuda_graphs=False)
+    ref = e1.generate_speculative(prompts, 10, NgramDrafter(), n_draft=5)
+    e2 = Engine(cfg, device="cuda", model=e1.model, num_pages=32, page_size=64, cuda_graphs=True,
+                graph_buckets=(4, 12))
+    out = e2.generate_speculative(prompts, 10, NgramDrafter(), n_draft=5)
+    assert out == ref
+    assert len(e2._graphs) > 0                  # verify rows ran in captured decode graphs
