@@ -222,3 +222,22 @@ def test_speculative_verify_in_decode_graph():
     out = e2.generate_speculative(prompts, 10, NgramDrafter(), n_draft=5)
     assert out == ref
     assert len(e2._graphs) > 0                  # verify rows ran in captured decode graphs
+
+
+def test_v4_late_replay_vs_oracle():
+    """Bounded late-layer replay on the GPU engine: layer 2 of a 300-token prefill runs only the last 128 tokens;
+    the prefill logits follow the oracle of the same definition."""
+    cfg = _v4_cfg(n_layers=3).replace(late_layer_start=2, late_replay=128)
+    w = fp8_roundtrip(init_weights(cfg, seed=0))
+    ref = RefModel(cfg, w)
+    g = torch.Generator().manual_seed(1)
+    prompt = torch.randint(0, cfg.vocab_size, (300,), generator=g)
+    eng = Engine(cfg, device="cuda", source=WeightSource(cfg, state=w), num_pages=32, page_size=64)
+    eng.model.trace = []
+    r = eng.add_request(prompt.tolist())
+    got = eng.prefill([r])[0].float().cpu()
+    ref.forced_routing = {int(k.split(".")[0]): v.long() for k, v in eng.model.trace if k.endswith("router_ids")}
+    ref.forced_dsa = {int(k.split(".")[0]): v.long() for k, v in eng.model.trace if k.endswith("dsa_pos")}
+    exp = ref.forward(prompt)[-1]
+    assert _rel(got, exp) < 0.15, _rel(got, exp)
+    assert torch.corrcoef(torch.stack([got, exp]))[0, 1] > 0.98
