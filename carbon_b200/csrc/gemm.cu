@@ -3,6 +3,7 @@
 #include <mutex>
 #include "gemm.cuh"
 #include "gemm_pair.cuh"
+#include <cstdlib>
 #include "small_ops.h"
 
 namespace cb {
@@ -48,6 +49,17 @@ static bool make_tmap_sf(CUtensorMap* m, const uint32_t* sf, uint64_t rows, uint
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<uint32_t*>(sf), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// bf16 pair-GEMM epilogue choice: CARBON_GEMM_ROWS=1 stages the output tile in shared memory and stores it
+// row-contiguous (one fewer pipeline stage); 0 keeps row-per-lane stores.  Read once per process.
+static bool gemm_rows_epilogue() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("CARBON_GEMM_ROWS");
+    v = (e && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
 }
 
 // Launch of the pair-tile GEMM: clusters of PAIR CTAs, one persistent cluster per co-resident slot.
@@ -233,6 +245,8 @@ cudaError_t gemm_fp8(const void* A, const void* B, const uint32_t* sfa, const ui
     const int units = (m_block_expert ? max_m_blocks / 2 : ceil_div(M, 256)) * ceil_div(N, 256);
     if (epi == GEMM_OUT_SWIGLU_FP8)
       return launch_pair<KIND_MXF8, EPI_SWIGLU_FP8, 2, 6>(ta, tb, tsa, tsb, p, units, num_sms, s);
+    if (gemm_rows_epilogue() && ldo % 8 == 0 && N % 8 == 0)      // row-contiguous staged stores (5 stages)
+      return launch_pair<KIND_MXF8, EPI_BF16_ROWS, 2, 5>(ta, tb, tsa, tsb, p, units, num_sms, s);
     return launch_pair<KIND_MXF8, EPI_BF16, 2, 6>(ta, tb, tsa, tsb, p, units, num_sms, s);
   }
   if (pair == 2 && m_block_expert) {

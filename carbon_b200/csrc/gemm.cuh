@@ -21,7 +21,9 @@
 namespace cb {
 
 enum GemmKind { KIND_MXF8 = 0, KIND_BF16 = 1 };
-enum GemmEpi { EPI_BF16 = 0, EPI_SWIGLU_FP8 = 1, EPI_F32 = 2, EPI_INDEXER = 3, EPI_BF16_SCATTER = 4 };
+// EPI_BF16_ROWS: EPI_BF16 with the output staged in shared memory and stored row-contiguous (pair kernel only)
+enum GemmEpi { EPI_BF16 = 0, EPI_SWIGLU_FP8 = 1, EPI_F32 = 2, EPI_INDEXER = 3, EPI_BF16_SCATTER = 4,
+               EPI_BF16_ROWS = 5 };
 
 struct GemmParams {
   int M, N, K;                 // N = per-expert N in grouped mode

@@ -57,7 +57,8 @@ template <int KIND, int PAIR, int STAGES, int EPI = EPI_BF16>
 constexpr int gemm_pair_smem_bytes() {
   using C = PairCfg<KIND, PAIR, EPI>;
   return 1024 + STAGES * (C::TILE_A + C::TILE_B + C::SFA_BYTES + C::SFB_BYTES) + 8 * (2 * STAGES + 8) + 16 +
-         2 * 2 * 128 * 4 + (EPI == EPI_BF16_SCATTER ? 16 + C::kEpiWarps * kScatterWarpBytes : 0);
+         2 * 2 * 128 * 4 +
+         (EPI == EPI_BF16_SCATTER || EPI == EPI_BF16_ROWS ? 16 + C::kEpiWarps * kScatterWarpBytes : 0);
 }
 
 template <int KIND, int EPI, int PAIR, int STAGES>
@@ -70,7 +71,8 @@ __global__ void __launch_bounds__(PairCfg<KIND, PAIR, EPI>::kThreads, 1)
   constexpr int BN = C::BN, BM = C::BM, BK = C::BK;
   constexpr bool kScaled = C::kScaled;
   constexpr int kMmaPerStage = BK / C::UMMA_K;
-  static_assert(EPI == EPI_BF16 || EPI == EPI_BF16_SCATTER || EPI == EPI_SWIGLU_FP8 || EPI == EPI_INDEXER,
+  static_assert(EPI == EPI_BF16 || EPI == EPI_BF16_SCATTER || EPI == EPI_BF16_ROWS || EPI == EPI_SWIGLU_FP8 ||
+                    EPI == EPI_INDEXER,
                 "pair GEMM epilogues");
   static_assert(EPI != EPI_SWIGLU_FP8 || kScaled, "SwiGLU requant epilogue follows an fp8 GEMM");
 
@@ -306,18 +308,23 @@ __global__ void __launch_bounds__(PairCfg<KIND, PAIR, EPI>::kThreads, 1)
       const bool ovl_first = C::kOvl > 0 && s == 0 && h == 1;       // stage 0: local columns [224,256)
       const bool ovl_owner = C::kOvl > 0 && ((s == 0 && h == 1) || (s == 1 && h == 0));
 
-      if constexpr (EPI == EPI_BF16_SCATTER) {
-        // Rows go to their owners over NVLink.  A row-per-lane store would put 32 rows' 16-byte pieces into one
-        // warp instruction, i.e. 32 small NVLink writes; instead each 64-column slab of the warp's 32 rows is
-        // staged in shared memory and written back row-contiguous: one instruction covers four 128-byte row
-        // segments.  (Requires ldo % 8 == 0 and N % 8 == 0, checked by the host.)
+      if constexpr (EPI == EPI_BF16_SCATTER || EPI == EPI_BF16_ROWS) {
+        // A row-per-lane store would put 32 rows' 16-byte pieces into one warp instruction: 32 small NVLink writes
+        // (scatter: rows go to their owners' slots in peer HBM) or 32 partial-sector L2 writes (local rows).
+        // Instead each 64-column slab of the warp's 32 rows is staged in shared memory and written back
+        // row-contiguous: one instruction covers four 128-byte row segments.  (Requires ldo % 8 == 0 and
+        // N % 8 == 0, checked by the host.)
         uint8_t* stg = xstage + (warp - 4) * kScatterWarpBytes;
         __nv_bfloat16* my_base = nullptr;
         if (row_ok) {
-          int r = 0;
-          while (r + 1 < p.scatter_world && row >= p.scatter_bounds[r + 1]) ++r;
-          my_base = reinterpret_cast<__nv_bfloat16*>(p.scatter_ptrs[r]) +
-                    (size_t(p.scatter_rank) * p.scatter_rows + (row - p.scatter_bounds[r])) * size_t(p.ldo);
+          if constexpr (EPI == EPI_BF16_SCATTER) {
+            int r = 0;
+            while (r + 1 < p.scatter_world && row >= p.scatter_bounds[r + 1]) ++r;
+            my_base = reinterpret_cast<__nv_bfloat16*>(p.scatter_ptrs[r]) +
+                      (size_t(p.scatter_rank) * p.scatter_rows + (row - p.scatter_bounds[r])) * size_t(p.ldo);
+          } else {
+            my_base = reinterpret_cast<__nv_bfloat16*>(p.out) + size_t(row) * p.ldo;
+          }
         }
         const uint64_t my_base_u = reinterpret_cast<uint64_t>(my_base);
 #pragma unroll 1
