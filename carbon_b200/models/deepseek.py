@@ -428,16 +428,20 @@ class DeepseekModel:
         q_lat_a = q_lat_l.to(self.act_dtype) if self.on_gpu else q_lat_l
         if dp:
             q_lat, latent = q_lat_a, latent_l
-            idx_k = idx_l[1] if idx_l is not None else None
-            out_loc = fb.out_loc[lo:hi]
+            # every rank's cache receives every token's rows (one all-gather of the new rows): a later step may
+            # give a request to another rank (prefill shards by tokens, decode by rows)
+            with region("dp.kv_gather"):
+                latent_c = pc.gather_rows(latent_l)
+                idx_k = pc.gather_rows(idx_l[1]) if idx_l is not None else None
         else:
             with region("tp.gather"):
                 q_lat = pc.gather_rows(q_lat_a)
                 latent = pc.gather_rows(latent_l)
                 idx_k = pc.gather_rows(idx_l[1]) if idx_l is not None else None
-            out_loc = fb.out_loc
+            latent_c = latent
+        out_loc = fb.out_loc
         with region("attn.kv_proj"):
-            cache.write_latent(i, out_loc, latent)
+            cache.write_latent(i, out_loc, latent_c)
             if idx_k is not None:
                 cache.write_index_k(i, out_loc, idx_k)
         T = q_lat.shape[0]

@@ -23,9 +23,12 @@ def _free_port():
     return p
 
 
-def _prompts(cfg):
+def _prompts(cfg, variant="v3"):
     g = torch.Generator().manual_seed(1)
-    return [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (64, 50, 70)]
+    # "skewed": prefill shards by tokens (rank 0: the 200-token prompt; rank 1: the short ones) but decode shards by
+    # rows (rank 0: requests 0-1), so request 1 decodes on a rank that did not prefill it
+    lens = (200, 10, 10) if variant == "skewed" else (64, 50, 70)
+    return [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in lens]
 
 
 def _cfg(variant):
@@ -49,19 +52,20 @@ def _worker(rank, world, port, q, attn_dp=False, variant="v3"):
         w = init_weights(cfg, seed=0)
         eng = Engine(cfg, device="cpu", source=WeightSource(cfg, state=w), num_pages=32, page_size=16,
                      pctx=DistCtx(rank, world, attn_dp=attn_dp))
-        outs, hist = eng.generate(_prompts(cfg), max_new_tokens=6, return_logits=True)
+        outs, hist = eng.generate(_prompts(cfg, variant), max_new_tokens=6, return_logits=True)
         q.put((rank, outs, [h.numpy().copy() for h in hist]))
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.parametrize("world,attn_dp,variant", [(2, False, "v3"), (2, True, "v3"), (2, False, "v4"),
-                                                   (2, True, "v4"), (2, False, "v4_late"), (2, True, "v4_late")])
+                                                   (2, True, "v4"), (2, False, "v4_late"), (2, True, "v4_late"),
+                                                   (2, True, "skewed"), (2, False, "skewed")])
 def test_tp_ep_engine_matches_single_rank(world, attn_dp, variant):
     cfg = _cfg(variant)
     w = init_weights(cfg, seed=0)
     single = Engine(cfg, device="cpu", source=WeightSource(cfg, state=w), num_pages=32, page_size=16)
-    outs_ref, hist_ref = single.generate(_prompts(cfg), max_new_tokens=6, return_logits=True)
+    outs_ref, hist_ref = single.generate(_prompts(cfg, variant), max_new_tokens=6, return_logits=True)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
