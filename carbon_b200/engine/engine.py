@@ -118,12 +118,14 @@ class Engine:
 
     # -- steps ---------------------------------------------------------------------------------------------------------
     def prefill(self, reqs: List[Request]) -> torch.Tensor:
-        """Run every request's uncached prompt tokens; returns logits [B, V] of each request's last token."""
+        """Run every request's uncached prompt tokens; returns logits [B, V] of each request's last token.  Requests
+        with a cached prefix (chunked prefill, prefix reuse) continue through per-row attention over the cache."""
+        if any(r.n_cached > 0 for r in reqs):
+            return self._prefill_rows(reqs, [r.seq_len - r.n_cached for r in reqs])
         dev = self.device
         ids, starts, lens = [], [], []
         for r in reqs:
             toks = (r.prompt + r.out)[r.n_cached:]
-            assert r.n_cached == 0, "prefill with a cached prefix is not supported by this step"
             self._ensure_pages(r, r.seq_len)
             ids += toks
             starts.append(r.n_cached)
@@ -145,6 +147,51 @@ class Engine:
             r.n_cached += n
         self.stats["prefill_tokens"] += sum(lens)
         return logits
+
+    def prefill_chunked(self, reqs: List[Request], chunk: int) -> torch.Tensor:
+        """Chunked prefill: each step runs at most ``chunk`` uncached prompt tokens per request, every token attending
+        to its request's cached keys (the reference bounds a prefill step at 131,072 tokens, 32,768 per rank).
+        Returns logits [B, V] of each request's last prompt token."""
+        if self.cfg.late_layer_start >= 0:
+            for r in reqs:                      # the replayed tail is fixed by the whole prompt
+                r.late_from = max(0, r.seq_len - self.cfg.late_replay)
+        out = [None] * len(reqs)
+        while True:
+            todo = [(b, r) for b, r in enumerate(reqs) if r.n_cached < r.seq_len]
+            if not todo:
+                break
+            n = [min(chunk, r.seq_len - r.n_cached) for _, r in todo]
+            lg = self._prefill_rows([r for _, r in todo], n)
+            for (b, r), row in zip(todo, lg):
+                if r.n_cached == r.seq_len:
+                    out[b] = row
+        return torch.stack(out)
+
+    def _prefill_rows(self, reqs: List[Request], counts: List[int]) -> torch.Tensor:
+        """Run the next ``counts[b]`` uncached tokens of each request as per-row attention over the paged cache
+        (keys: the request's cached tokens and the rows before it).  Returns logits [B, V] of each request's last
+        row of this step."""
+        rows_pt, rows_len, ids, late, last = [], [], [], [], []
+        for r, n in zip(reqs, counts):
+            toks = (r.prompt + r.out)[r.n_cached:r.n_cached + n]
+            self._ensure_pages(r, r.n_cached + n)
+            for j, tok in enumerate(toks):
+                rows_pt.append(r.pages)
+                rows_len.append(r.n_cached + j + 1)
+                ids.append(int(tok))
+                late.append(r.late_from)
+            last.append(len(ids) - 1)
+        m = len(ids)
+        out_loc, key_slots, n_keys, pos = decode_metadata(rows_pt, rows_len, self.page_size, m)
+        dev = self.device
+        fb = ForwardBatch(ids=torch.tensor(ids, dtype=torch.int32).to(dev), pos=pos.to(dev), out_loc=out_loc.to(dev),
+                          is_prefill=False, key_slots=key_slots.to(dev), n_keys=n_keys.to(dev),
+                          bounds=self._bounds([1] * m), late_from=torch.tensor(late, dtype=torch.int32).to(dev))
+        logits = self.model.forward(fb, self.cache)
+        for r, n in zip(reqs, counts):
+            r.n_cached += n
+        self.stats["prefill_tokens"] += m
+        return logits[torch.tensor(last, dtype=torch.long, device=logits.device)]
 
     def decode(self, reqs: List[Request], next_tokens: Sequence[int]) -> torch.Tensor:
         """Append one token per request and run it; returns logits [B, V]."""
