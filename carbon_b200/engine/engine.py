@@ -99,6 +99,9 @@ class Engine:
         self.graph_buckets = sorted(graph_buckets)
         self._graphs: Dict[int, "_DecodeGraph"] = {}
         self.stats = {"prefill_tokens": 0, "decode_tokens": 0}
+        from ..utils.metrics import Metrics
+
+        self.metrics = Metrics()       # device-timed steps: summary(), json_line(), prometheus()
 
     # -- request lifecycle -------------------------------------------------------------------------------------------
     def add_request(self, prompt: Sequence[int]) -> Request:
@@ -142,7 +145,8 @@ class Engine:
                           pos=pos.to(dev, non_blocking=True), out_loc=out_loc.to(dev, non_blocking=True),
                           is_prefill=True, cu_seqlens=cu, logits_rows=rows.to(dev, non_blocking=True),
                           bounds=self._bounds(lens))
-        logits = self.model.forward(fb, self.cache)
+        with self.metrics.step("prefill", sum(lens), len(reqs)):
+            logits = self.model.forward(fb, self.cache)
         for r, n in zip(reqs, lens):
             r.n_cached += n
         self.stats["prefill_tokens"] += sum(lens)
@@ -187,7 +191,8 @@ class Engine:
         fb = ForwardBatch(ids=torch.tensor(ids, dtype=torch.int32).to(dev), pos=pos.to(dev), out_loc=out_loc.to(dev),
                           is_prefill=False, key_slots=key_slots.to(dev), n_keys=n_keys.to(dev),
                           bounds=self._bounds([1] * m), late_from=torch.tensor(late, dtype=torch.int32).to(dev))
-        logits = self.model.forward(fb, self.cache)
+        with self.metrics.step("prefill", m, len(reqs)):
+            logits = self.model.forward(fb, self.cache)
         for r, n in zip(reqs, counts):
             r.n_cached += n
         self.stats["prefill_tokens"] += m
@@ -206,15 +211,16 @@ class Engine:
         ids[:B] = torch.tensor([r.out[-1] for r in reqs], dtype=torch.int32)
         late = torch.zeros(bucket, dtype=torch.int32)
         late[:B] = torch.tensor([r.late_from for r in reqs], dtype=torch.int32)
-        if self.cuda_graphs and bucket is not None:
-            g = self._graph(bucket, key_slots.shape[1])
-            logits = g.run(ids, pos, out_loc, key_slots, n_keys, late)[:B]
-        else:
-            dev = self.device
-            fb = ForwardBatch(ids=ids.to(dev), pos=pos.to(dev), out_loc=out_loc.to(dev), is_prefill=False,
-                              key_slots=key_slots.to(dev), n_keys=n_keys.to(dev), bounds=self._bounds([1] * bucket),
-                              late_from=late.to(dev))
-            logits = self.model.forward(fb, self.cache)[:B]
+        with self.metrics.step("decode", B, B):
+            if self.cuda_graphs and bucket is not None:
+                g = self._graph(bucket, key_slots.shape[1])
+                logits = g.run(ids, pos, out_loc, key_slots, n_keys, late)[:B]
+            else:
+                dev = self.device
+                fb = ForwardBatch(ids=ids.to(dev), pos=pos.to(dev), out_loc=out_loc.to(dev), is_prefill=False,
+                                  key_slots=key_slots.to(dev), n_keys=n_keys.to(dev),
+                                  bounds=self._bounds([1] * bucket), late_from=late.to(dev))
+                logits = self.model.forward(fb, self.cache)[:B]
         for r in reqs:
             r.n_cached = r.seq_len
         self.stats["decode_tokens"] += B
@@ -243,18 +249,20 @@ class Engine:
         bucket = self._bucket(n) if self.cuda_graphs else None
         out_loc, key_slots, n_keys, pos = decode_metadata(rows_pt, rows_len, self.page_size, bucket or n)
         dev = self.device
-        if bucket is not None:
-            ids_t = torch.zeros(bucket, dtype=torch.int32)
-            ids_t[:n] = torch.tensor(ids, dtype=torch.int32)
-            late_t = torch.zeros(bucket, dtype=torch.int32)
-            late_t[:n] = torch.tensor(late, dtype=torch.int32)
-            logits = self._graph(bucket, key_slots.shape[1]).run(ids_t, pos, out_loc, key_slots, n_keys, late_t)[:n]
-        else:
-            fb = ForwardBatch(ids=torch.tensor(ids, dtype=torch.int32).to(dev), pos=pos.to(dev),
-                              out_loc=out_loc.to(dev), is_prefill=False, key_slots=key_slots.to(dev),
-                              n_keys=n_keys.to(dev), bounds=self._bounds([1] * n),
-                              late_from=torch.tensor(late, dtype=torch.int32).to(dev))
-            logits = self.model.forward(fb, self.cache)
+        with self.metrics.step("verify", n, len(reqs)):
+            if bucket is not None:
+                ids_t = torch.zeros(bucket, dtype=torch.int32)
+                ids_t[:n] = torch.tensor(ids, dtype=torch.int32)
+                late_t = torch.zeros(bucket, dtype=torch.int32)
+                late_t[:n] = torch.tensor(late, dtype=torch.int32)
+                logits = self._graph(bucket, key_slots.shape[1]).run(ids_t, pos, out_loc, key_slots, n_keys,
+                                                                     late_t)[:n]
+            else:
+                fb = ForwardBatch(ids=torch.tensor(ids, dtype=torch.int32).to(dev), pos=pos.to(dev),
+                                  out_loc=out_loc.to(dev), is_prefill=False, key_slots=key_slots.to(dev),
+                                  n_keys=n_keys.to(dev), bounds=self._bounds([1] * n),
+                                  late_from=torch.tensor(late, dtype=torch.int32).to(dev))
+                logits = self.model.forward(fb, self.cache)
         pred = torch.argmax(logits.float(), dim=-1).tolist()
         accepted, i = [], 0
         for r, t, d in zip(reqs, last_tokens, drafts):
