@@ -34,6 +34,26 @@ enum : int {
   kErrBadArg = 5,
 };
 
+// Bounds-checked debug builds (compute-sanitizer is not available everywhere): building with
+// CARBON_DEBUG_BOUNDS=1 defines CB_DEBUG_BOUNDS.  Index-driven kernels pass every row index they compute through
+// cb_check_index() and skip the access when it fails; a debug build also prints the first failure of each
+// translation unit (kernel site, index, limit, block, thread), so a wrong index shows up as one stderr line instead
+// of a fault.  Release builds keep only the range test.
+#ifdef CB_DEBUG_BOUNDS
+static __device__ int cb_bounds_reported = 0;
+__device__ __forceinline__ bool cb_check_index(long long idx, long long limit, const char* site) {
+  if (idx >= 0 && idx < limit) return true;
+  if (atomicCAS(&cb_bounds_reported, 0, 1) == 0)
+    printf("[carbon bounds] %s: index %lld outside [0, %lld) (block %d thread %d)\n", site, idx, limit,
+           int(blockIdx.x), int(threadIdx.x));
+  return false;
+}
+#else
+__device__ __forceinline__ bool cb_check_index(long long idx, long long limit, const char*) {
+  return idx >= 0 && idx < limit;
+}
+#endif
+
 CB_DEVICE float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -27,12 +27,16 @@ __global__ void engram_gather_kernel(const int* __restrict__ ids, int T, int C, 
   if (item >= T * C) return;
   const int t = item / C, c = item - t * C;
   const int id = ids[item];
+  __nv_bfloat16* o = out + (size_t(t) * C + c) * dim;
+  if (!cb_check_index(id, bounds[world], "engram_gather")) {       // bad row id: a zero row, no access
+    for (int e0 = lane * 8; e0 < dim; e0 += 256) *reinterpret_cast<uint4*>(o + e0) = make_uint4(0, 0, 0, 0);
+    return;
+  }
   int r = 0;
   while (r + 1 < world && id >= bounds[r + 1]) ++r;
   const int local = id - bounds[r];
   const uint8_t* row = reinterpret_cast<const uint8_t*>(data_ptrs[r]) + size_t(local) * dim;
   const uint8_t* sf = reinterpret_cast<const uint8_t*>(sf_ptrs[r]) + size_t(local) * (dim / 32);
-  __nv_bfloat16* o = out + (size_t(t) * C + c) * dim;
   for (int e0 = lane * 8; e0 < dim; e0 += 256) {
     const uint2 raw = *reinterpret_cast<const uint2*>(row + e0);
     const float scale = __uint_as_float(uint32_t(sf[e0 / 32]) << 23);        // 2^(sf - 127)

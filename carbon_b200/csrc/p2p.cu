@@ -385,7 +385,8 @@ __global__ void embed_peer_kernel(const uint64_t* __restrict__ table_ptrs, int p
                                   float* __restrict__ sumsq) {
   __shared__ float red[32];
   const int t = blockIdx.x;
-  const int id = ids[t];
+  int id = ids[t];
+  if (!cb_check_index(id, (long long)per * world, "embed_peer")) id = 0;   // bad token id: row 0, no wild read
   int owner = id / per;
   if (owner >= world) owner = world - 1;
   const __nv_bfloat16* row = reinterpret_cast<const __nv_bfloat16*>(table_ptrs[owner]) + size_t(id - owner * per) * D;

@@ -103,7 +103,7 @@ __global__ void gather_fp8_rows_kernel(const uint8_t* __restrict__ src, const ui
   if (row >= M) return;
   if (n_blocks && row >= n_blocks[0] * 128) return;
   int sr = src_rows[row];
-  if (sr >= src_rows_n) sr = -1;
+  if (sr >= 0 && !cb_check_index(sr, src_rows_n, "gather_fp8_rows")) sr = -1;
   const uint4* s4 = reinterpret_cast<const uint4*>(src + size_t(sr < 0 ? 0 : sr) * K);
   uint4* d4 = reinterpret_cast<uint4*>(dst + size_t(row) * K);
   for (int c = lane; c < K / 16; c += 32) d4[c] = sr < 0 ? make_uint4(0, 0, 0, 0) : s4[c];

@@ -20,6 +20,8 @@ NVCC_FLAGS = [
     "-Xptxas=-v" if os.environ.get("CARBON_PTXAS_V") else "-Xptxas=-O3",
 ]
 CXX_FLAGS = ["-O3", "-std=c++17", "-DNDEBUG"]
+if os.environ.get("CARBON_DEBUG_BOUNDS") == "1":       # bounds-checked debug build (see csrc/common.cuh)
+    NVCC_FLAGS.append("-DCB_DEBUG_BOUNDS")
 
 sources = sorted(glob.glob(os.path.join(CSRC, "*.cu"))) + sorted(glob.glob(os.path.join(CSRC, "*.cpp")))
 
