@@ -51,13 +51,14 @@ static bool make_tmap_sf(CUtensorMap* m, const uint32_t* sf, uint64_t rows, uint
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// bf16 pair-GEMM epilogue choice: CARBON_GEMM_ROWS=1 stages the output tile in shared memory and stores it
-// row-contiguous (one fewer pipeline stage); 0 keeps row-per-lane stores.  Read once per process.
+// bf16 pair-GEMM epilogue: the output tile is staged in shared memory and stored row-contiguous (one fewer
+// pipeline stage).  Measured on B200 (CUDA events): 8192x8192x7168 2954 -> 3183 TFLOP/s, 16384x7168x2048
+// 2225 -> 2882 TFLOP/s, 16k-token MoE layer 5.65 -> 5.17 ms.  CARBON_GEMM_ROWS=0 restores row-per-lane stores.
 static bool gemm_rows_epilogue() {
   static int v = -1;
   if (v < 0) {
     const char* e = getenv("CARBON_GEMM_ROWS");
-    v = (e && e[0] == '1') ? 1 : 0;
+    v = (e && e[0] == '0') ? 0 : 1;
   }
   return v == 1;
 }
