@@ -53,12 +53,17 @@ struct PairCfg {
 constexpr int kScatterRowBytes = 144;
 constexpr int kScatterWarpBytes = 32 * kScatterRowBytes;
 
+// SwiGLU epilogue staging: per TMEM lane quadrant the 32 rows x 128 fp8 output bytes of a tile (both column
+// halves), rows padded to 144 bytes
+constexpr int kSwiQuadBytes = 32 * kScatterRowBytes;
+
 template <int KIND, int PAIR, int STAGES, int EPI = EPI_BF16>
 constexpr int gemm_pair_smem_bytes() {
   using C = PairCfg<KIND, PAIR, EPI>;
   return 1024 + STAGES * (C::TILE_A + C::TILE_B + C::SFA_BYTES + C::SFB_BYTES) + 8 * (2 * STAGES + 8) + 16 +
          2 * 2 * 128 * 4 +
-         (EPI == EPI_BF16_SCATTER || EPI == EPI_BF16_ROWS ? 16 + C::kEpiWarps * kScatterWarpBytes : 0);
+         (EPI == EPI_BF16_SCATTER || EPI == EPI_BF16_ROWS ? 16 + C::kEpiWarps * kScatterWarpBytes : 0) +
+         (EPI == EPI_SWIGLU_FP8 ? 16 + 4 * kSwiQuadBytes + 4 * 8 : 0);
 }
 
 template <int KIND, int EPI, int PAIR, int STAGES>
@@ -93,6 +98,8 @@ __global__ void __launch_bounds__(PairCfg<KIND, PAIR, EPI>::kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_smem + 1);
   float* xamax = reinterpret_cast<float*>(tmem_base_smem + 4);   // [2 tiles][2 halves][128 rows]
   uint8_t* xstage = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(xamax + 2 * 2 * 128) + 15) & ~uintptr_t(15));
+  // SwiGLU: one mbarrier per TMEM lane quadrant pairs its two epilogue warps around the staging rows (bounded waits)
+  uint64_t* qbar = reinterpret_cast<uint64_t*>(xstage + 4 * kSwiQuadBytes);
 
   const uint32_t warp = warp_id();
   const uint32_t lane = lane_id();
@@ -106,6 +113,8 @@ __global__ void __launch_bounds__(PairCfg<KIND, PAIR, EPI>::kThreads, 1)
       mbar_init(&tempty_ovl[i], (C::kEpiWarps / 2) * PAIR);
     }
     mbar_init(xbar, 32 * C::kEpiWarps);
+    if constexpr (EPI == EPI_SWIGLU_FP8)
+      for (int i = 0; i < 4; ++i) mbar_init(&qbar[i], 64);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -425,15 +434,17 @@ __global__ void __launch_bounds__(PairCfg<KIND, PAIR, EPI>::kThreads, 1)
         mbar_arrive(xbar);
         if (!mbar_wait(xbar, j & 1)) { fail(kErrTimeoutTmem); break; }
         amax = fmaxf(amax, xa[(h ^ 1) * 128 + row_in_cta]);
-        if (row_ok) {
+        {
+          // quantised bytes of both column halves meet in the quadrant's staging rows; the two warps of the
+          // quadrant then store whole 128-byte row segments (16 rows each), not 16-byte pieces of 32 rows
           const uint32_t sb = ue8m0_for_amax(amax);
           const float inv = ue8m0_inv(sb);
-          uint8_t* orow = reinterpret_cast<uint8_t*>(p.out) + size_t(row) * p.ldo + nb * 128;
+          uint8_t* qst = xstage + q * kSwiQuadBytes;
 #pragma unroll
           for (int i = 0; i < 2; ++i) {
             const float* a = i == 0 ? a0 : a1;
             const int oc = i == 0 ? oc0 : 1 - oc0;
-            uint4* o = reinterpret_cast<uint4*>(orow + 64 * h + 32 * oc);
+            uint4* o = reinterpret_cast<uint4*>(qst + lane * kScatterRowBytes + 64 * h + 32 * oc);
 #pragma unroll
             for (int jj = 0; jj < 2; ++jj) {
               uint4 w;
@@ -444,6 +455,24 @@ __global__ void __launch_bounds__(PairCfg<KIND, PAIR, EPI>::kThreads, 1)
               o[jj] = w;
             }
           }
+          // each processed tile completes qbar[q] twice (staged, then stored): parities 0 and 1
+          mbar_arrive(&qbar[q]);
+          if (!mbar_wait(&qbar[q], 0)) { fail(kErrTimeoutTmem); break; }
+          const int row0 = mb * BM + int(rank) * 128 + int(q) * 32;     // first row of this quadrant
+#pragma unroll
+          for (int it = 0; it < 4; ++it) {
+            const int r = 16 * int(h) + 4 * it + int(lane >> 3);          // this warp's 16 rows, 4 per instruction
+            const int ok = __shfl_sync(0xffffffffu, row_ok ? 1 : 0, r);    // lane r of either warp owns row r
+            const uint4 w = *reinterpret_cast<const uint4*>(qst + r * kScatterRowBytes + (lane & 7) * 16);
+            if (ok)
+              *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.out) + size_t(row0 + r) * p.ldo + nb * 128 +
+                                        (lane & 7) * 16) = w;
+          }
+          mbar_arrive(&qbar[q]);                                           // staging free for the next tile
+          if (!mbar_wait(&qbar[q], 1)) { fail(kErrTimeoutTmem); break; }
+        }
+        if (row_ok) {
+          const uint32_t sb = ue8m0_for_amax(amax);
           if (h == 0) {
             const int kbo = nb;                               // output k-block (128 columns per tile)
             const int rb = row / 128, r = row % 128;
