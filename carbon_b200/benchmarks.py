@@ -74,11 +74,14 @@ def bench_attn(a):
         qi = torch.randn(T, 64, 128, device="cuda").to(torch.float8_e4m3fn).to(torch.bfloat16)
         ki = torch.randn(T, 128, device="cuda").to(torch.float8_e4m3fn).to(torch.bfloat16)
         wi = torch.randn(T, 64, device="cuda") * (64 ** -0.5) * (128 ** -0.5)
-        ms = time_fn(lambda: indexer_prefill_mask(qi, ki, wi, cu, a.topk), iters=5)
-        mask = indexer_prefill_mask(qi, ki, wi, cu, a.topk)
+        # fp8 e4m3 inputs (the config's indexer precision): block-scaled fp8 logits; bf16 kernel for comparison
+        fp8 = not a.indexer_bf16
+        ms = time_fn(lambda: indexer_prefill_mask(qi, ki, wi, cu, a.topk, fp8=fp8), iters=5)
+        mask = indexer_prefill_mask(qi, ki, wi, cu, a.topk, fp8=fp8)
         idx_flops = B * (S * S / 2) * 64 * 128 * 2
         res["indexer_ms"] = round(ms, 3)
         res["indexer_tflops"] = round(idx_flops / ms / 1e9, 1)
+        res["indexer_inputs"] = "fp8 e4m3" if fp8 else "bf16"
     ms = time_fn(lambda: mla_prefill(q, kvb, kpe, cu, 192 ** -0.5, mask, version=a.attn_version), iters=5)
     flops = B * H * (S * S / 2) * (192 + 128) * 2
     pk = peaks()
@@ -231,6 +234,7 @@ def main(argv=None):
     ap.add_argument("--seq", type=int, default=8192)
     ap.add_argument("--heads", type=int, default=128)
     ap.add_argument("--dsa", action="store_true")
+    ap.add_argument("--indexer-bf16", action="store_true", help="attn --dsa: bf16 indexer logits instead of fp8")
     ap.add_argument("--topk", type=int, default=2048, help="DSA top-k")
     ap.add_argument("--moe-topk", type=int, default=8, help="router top-k (moe)")
     ap.add_argument("--context", type=int, default=4096)

@@ -47,6 +47,9 @@ class ModelConfig:
     # indexer q and k in MXFP4 (e2m1 + UE8M0 per 32 dims; the reference's 68-byte index keys,
     # dec/cuda_paged_logits.py:35-37): both are rounded to fp4 values before the logits
     index_fp4: bool = False
+    # indexer q and k in fp8 e4m3 with one UE8M0 scale per 128-dim row (per head for q), the DeepSeek-V3.2 indexer
+    # precision: the prefill logits run as block-scaled fp8 tcgen05 MMAs; decode sees the same rounded values
+    index_fp8: bool = False
     # per-head learned attention sink: one extra logit in each softmax denominator (attn.sink [n_heads] fp32)
     attn_sink: bool = False
     # attention kind.  "mla": q/k = [nope | RoPE] per head, keys and values up-projected from the kv latent (wkv_b);

@@ -295,6 +295,21 @@ void indexer_logits(torch::Tensor keys, torch::Tensor q, torch::Tensor w, torch:
                         cur_stream()));
 }
 
+// fp8 keys kq [L, Di] + ksf, queries qq [Tq*H, Di] + qsf (act_quant SF tiles), w [Tq, H] -> logits [Tq, ldo] fp32
+void indexer_logits_fp8(torch::Tensor kq, torch::Tensor ksf, torch::Tensor qq, torch::Tensor qsf, int64_t H,
+                        torch::Tensor w, torch::Tensor out, bool causal) {
+  CHECK_CUDA(kq); CHECK_CONTIG(kq); CHECK_CONTIG(qq); CHECK_CONTIG(w); CHECK_DT(w, at::kFloat);
+  CHECK_DT(out, at::kFloat);
+  TORCH_CHECK(kq.element_size() == 1 && qq.element_size() == 1 && kq.size(1) == qq.size(1));
+  const int Tq = int(qq.size(0) / H);
+  TORCH_CHECK(out.stride(1) == 1 && out.size(0) >= Tq && out.stride(0) >= kq.size(0));
+  c10::cuda::CUDAGuard g(kq.device());
+  CK(cb::indexer_logits_fp8(kq.data_ptr(), reinterpret_cast<const uint32_t*>(ksf.data_ptr()), kq.size(0),
+                            qq.data_ptr(), reinterpret_cast<const uint32_t*>(qsf.data_ptr()), Tq, int(H),
+                            int(kq.size(1)), w.data_ptr<float>(), out.data_ptr<float>(), out.stride(0), causal,
+                            nullptr, num_sms(), cur_stream()));
+}
+
 void topk_mask(torch::Tensor logits, int64_t Tq, int64_t k, torch::Tensor mask, int64_t row0) {
   CHECK_CUDA(logits); CHECK_DT(logits, at::kFloat); CHECK_DT(mask, at::kInt); CHECK_CONTIG(mask);
   TORCH_CHECK(logits.stride(1) == 1 && row0 + Tq <= mask.size(0) && mask.size(1) * 32 >= Tq);
@@ -398,6 +413,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("launch_count", []() { return g_launches.load(); });
   m.def("attn_prefill", &attn_prefill);
   m.def("indexer_logits", &indexer_logits);
+  m.def("indexer_logits_fp8", &indexer_logits_fp8);
   m.def("topk_mask", &topk_mask);
   m.def("sparse_mla", &sparse_mla);
   m.def("engram_gather", &engram_gather);

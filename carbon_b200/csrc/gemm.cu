@@ -421,4 +421,31 @@ cudaError_t indexer_logits(const void* keys, int L, const void* q, int Tq, int H
   return launch_pair<KIND_BF16, EPI_INDEXER, 2, 6>(ta, tb, ta, tb, p, units, num_sms, s);
 }
 
+// The same with fp8 e4m3 keys and queries (1x128 UE8M0 scale per row, SF-tile layout of act_quant): block-scaled
+// tcgen05 MMAs at twice the bf16 rate.  keys [L, Di] fp8 + SF, q [Tq*H, Di] fp8 + SF.
+cudaError_t indexer_logits_fp8(const void* keys, const uint32_t* keys_sf, int L, const void* q, const uint32_t* q_sf,
+                               int Tq, int H, int Di, const float* w, float* out, int ldo, bool causal, int* status,
+                               int num_sms, cudaStream_t s) {
+  if (L <= 0 || Tq <= 0) return cudaSuccess;
+  constexpr int BN = 256;
+  if (Di % 128 || BN % H || H % 16) return cudaErrorInvalidValue;
+  if ((BN / H) % 2) return cudaErrorInvalidValue;
+  const int N = Tq * H;
+  CUtensorMap ta, tb, tsa, tsb;
+  if (!make_tmap_2d(&ta, keys, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, Di, L, Di, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tmap_2d(&tb, q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, Di, N, Di, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tmap_sf(&tsa, keys_sf, uint64_t(ceil_div(Di, 512)) * ceil_div(L, 128), 1) ||
+      !make_tmap_sf(&tsb, q_sf, uint64_t(ceil_div(Di, 512)) * ceil_div(N, 128), 2))
+    return cudaErrorInvalidValue;
+  GemmParams p{};
+  p.M = L; p.N = N; p.K = Di;
+  p.sfa = keys_sf; p.sfb = q_sf;
+  p.sfa_row_blocks = ceil_div(L, 128);
+  p.sfb_row_blocks = ceil_div(N, 128);
+  p.out = out; p.ldo = ldo; p.status = status;
+  p.idx_w = w; p.idx_heads = H; p.causal = causal ? 1 : 0;
+  const int units = ceil_div(L, 256) * ceil_div(N, BN);
+  return launch_pair<KIND_MXF8, EPI_INDEXER, 2, 6>(ta, tb, tsa, tsb, p, units, num_sms, s);
+}
+
 }  // namespace cb

@@ -110,7 +110,8 @@ __global__ void __launch_bounds__(PairCfg<KIND, PAIR, EPI>::kThreads, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&tfull_bar[i], 1);
       mbar_init(&tempty_full[i], C::kEpiWarps * PAIR);
-      mbar_init(&tempty_ovl[i], (C::kEpiWarps / 2) * PAIR);
+      // the indexer epilogue releases the overlap columns with the full drain (every warp arrives)
+      mbar_init(&tempty_ovl[i], (EPI == EPI_INDEXER ? C::kEpiWarps : C::kEpiWarps / 2) * PAIR);
     }
     mbar_init(xbar, 32 * C::kEpiWarps);
     if constexpr (EPI == EPI_SWIGLU_FP8)
@@ -521,6 +522,7 @@ __global__ void __launch_bounds__(PairCfg<KIND, PAIR, EPI>::kThreads, 1)
             *o = (p.causal && key > qi) ? -INFINITY : (acc4[0] + acc4[1]) + (acc4[2] + acc4[3]);
           }
         }
+        if constexpr (C::kOvl > 0) release(&tempty_ovl[s]);       // fp8 (scaled) layout: stages share 32 columns
         release(&tempty_full[s]);
       }
       ++j;

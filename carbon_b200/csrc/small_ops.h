@@ -68,6 +68,10 @@ cudaError_t attn_prefill3(const void* q, const void* kvb, const void* kpe, int T
 // DSA indexer: logits GEMM with fused relu/weight/head-sum epilogue (gemm.cu) and exact top-k bitmask (topk.cu)
 cudaError_t indexer_logits(const void* keys, int L, const void* q, int Tq, int H, int Di, const float* w, float* out,
                            int ldo, bool causal, int* status, int num_sms, cudaStream_t s);
+// fp8 e4m3 keys [L, Di] / queries [Tq*H, Di] with 1x128 UE8M0 SF tiles (block-scaled tcgen05)
+cudaError_t indexer_logits_fp8(const void* keys, const uint32_t* keys_sf, int L, const void* q, const uint32_t* q_sf,
+                               int Tq, int H, int Di, const float* w, float* out, int ldo, bool causal, int* status,
+                               int num_sms, cudaStream_t s);
 cudaError_t topk_mask(const float* logits, int ldo, int Tq, int k, uint32_t* mask, int mask_words, int row0,
                       cudaStream_t s);
 cudaError_t indexer_decode_logits(const void* q, const float* w, const void* kc, const int* key_slots,

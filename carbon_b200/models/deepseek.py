@@ -487,6 +487,9 @@ class DeepseekModel:
         if cfg.index_fp4:               # fp4 values are exact in bf16: the bf16 logits kernels compute fp4 products
             q = R.fake_quant_mxfp4(q)
             k = R.fake_quant_mxfp4(k)
+        elif cfg.index_fp8:             # likewise e4m3 values (prefill re-quantises them exactly for fp8 MMAs)
+            q = R.fake_quant_fp8_rows(q)
+            k = R.fake_quant_fp8_rows(k)
         return q, k.view(T, Di), w
 
     def _prefill_key_masks(self, idx_l, fb: ForwardBatch, gather: bool = True):
@@ -499,7 +502,8 @@ class DeepseekModel:
         if lmax <= self.cfg.index_topk:
             return None
         q, k, w = idx_l
-        m = A.indexer_prefill_mask(q, k, w, cu_l if len(cu_l) > 1 else [0, 0], self.cfg.index_topk, lmax=lmax)
+        m = A.indexer_prefill_mask(q, k, w, cu_l if len(cu_l) > 1 else [0, 0], self.cfg.index_topk, lmax=lmax,
+                                   fp8=self.cfg.index_fp8 and k.shape[-1] % 128 == 0)
         return pc.gather_rows(m) if gather else m
 
     def _attn_prefill(self, i, q, latent, fb, idx_l, cache, dp: bool = False):

@@ -106,10 +106,11 @@ def unpack_key_mask(words: torch.Tensor, cu_seqlens: List[int]) -> List[torch.Te
 
 
 def indexer_prefill_mask(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, cu_seqlens: List[int],
-                         topk: int, lmax: Optional[int] = None) -> Optional[torch.Tensor]:
+                         topk: int, lmax: Optional[int] = None, fp8: bool = False) -> Optional[torch.Tensor]:
     """DSA selection for a prefill batch: per sequence, logits of every (query, causal key) pair and exact top-k.
     q [T, Hi, Di], k [T, Di], w [T, Hi]. Returns packed bits [T, ceil(Lmax/32)] (None when no sequence exceeds
-    top-k, i.e. attention stays dense causal)."""
+    top-k, i.e. attention stays dense causal).  fp8: q and k are quantised to e4m3 (1x128 UE8M0 per row) and the
+    logits run as block-scaled fp8 MMAs."""
     lens = [b - a for a, b in zip(cu_seqlens[:-1], cu_seqlens[1:])]
     lmax = max(lens) if lmax is None else lmax
     if lmax <= topk:
@@ -124,11 +125,19 @@ def indexer_prefill_mask(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, cu_s
             n = b - a
             ldo = (n + 3) // 4 * 4
             logits = torch.empty(n, ldo, dtype=torch.float32, device=q.device)
-            if n > topk:
+            if n > topk and fp8:
+                from .quant import quant_act
+
+                kq, ksf = quant_act(k[a:b].contiguous())
+                qq, qsf = quant_act(q[a:b].reshape(n * q.shape[1], q.shape[2]).contiguous())
+                e.indexer_logits_fp8(kq, ksf, qq, qsf, q.shape[1], w[a:b].float().contiguous(), logits, True)
+            elif n > topk:
                 e.indexer_logits(k[a:b].contiguous(), q[a:b].contiguous(), w[a:b].float().contiguous(), logits, True)
             e.topk_mask(logits, n, topk, mask, a)
         return mask
     masks = []
+    if fp8:
+        q, k = R.fake_quant_fp8_rows(q), R.fake_quant_fp8_rows(k)
     for a, b in zip(cu_seqlens[:-1], cu_seqlens[1:]):
         n = b - a
         pos = torch.arange(n)

@@ -212,6 +212,8 @@ class RefModel:
         wt = (h @ w[L + "weights_proj.weight"].t()) * (Hi ** -0.5) * (Di ** -0.5)
         if cfg.index_fp4:
             q, k = ops.fake_quant_mxfp4(q), ops.fake_quant_mxfp4(k)
+        elif cfg.index_fp8:
+            q, k = ops.fake_quant_fp8_rows(q), ops.fake_quant_fp8_rows(k)
         return q, k, wt
 
     def ffn(self, i: int, h: torch.Tensor) -> torch.Tensor:

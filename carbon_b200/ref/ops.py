@@ -100,6 +100,14 @@ def dequant_fp8_rows(q: torch.Tensor, s: torch.Tensor, block: int = 128) -> torc
     return q.float() * sf
 
 
+def fake_quant_fp8_rows(x: torch.Tensor) -> torch.Tensor:
+    """Round the last dim (a multiple of 128) to e4m3 with one UE8M0 scale per 128 elements, in x's dtype (the
+    values are exact in bf16)."""
+    shp = x.shape
+    q, s = quant_fp8_rows(x.reshape(-1, shp[-1]).float())
+    return dequant_fp8_rows(q, s).reshape(shp).to(x.dtype)
+
+
 def quant_fp8_blocks(w: torch.Tensor, block: int = 128) -> Tuple[torch.Tensor, torch.Tensor]:
     """128×128 weight quantisation. Returns (q [N,K], scale fp32 [ceil(N/128), ceil(K/128)])."""
     N, K = w.shape

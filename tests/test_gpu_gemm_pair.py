@@ -230,3 +230,27 @@ def test_gather_fp8_rows_matches_gather_quantise():
     torch.cuda.synchronize()
     assert torch.equal(q1.view(torch.uint8), q2.view(torch.uint8))
     assert torch.equal(sf1, sf2)
+
+
+@pytest.mark.parametrize("H", [64, 32])
+def test_indexer_logits_fp8(H):
+    """Block-scaled fp8 indexer logits (keys / queries in e4m3 with 1x128 UE8M0 scales) against the fp32 oracle of
+    the same fp8-rounded inputs."""
+    from carbon_b200.ops.quant import quant_act
+    from carbon_b200.ref import ops as R
+
+    torch.manual_seed(0)
+    L, Tq, Di = 700, 700, 128
+    k = torch.randn(L, Di).to(torch.bfloat16)
+    q = torch.randn(Tq, H, Di).to(torch.bfloat16)
+    w = torch.randn(Tq, H) * (H ** -0.5) * (Di ** -0.5)
+    kq, ksf = quant_act(k.cuda())
+    qq, qsf = quant_act(q.reshape(Tq * H, Di).cuda())
+    out = torch.empty(Tq, (L + 3) // 4 * 4, device="cuda")
+    _ext().indexer_logits_fp8(kq, ksf, qq, qsf, H, w.cuda(), out, True)
+    kf, qf = R.fake_quant_fp8_rows(k.float()), R.fake_quant_fp8_rows(q.float())
+    ref = R.indexer_logits(qf, kf, w)
+    causal = torch.arange(L)[None, :] <= torch.arange(Tq)[:, None]
+    got = out[:, :L].cpu()
+    assert torch.isinf(got[~causal]).all() and (got[~causal] < 0).all()
+    assert ((got[causal] - ref[causal]).norm() / ref[causal].norm()).item() < 1e-3
