@@ -1,0 +1,133 @@
+"""Continuous-batching scheduler over ``Engine`` (the serving loop the reference's engine provides around its
+prefill / decode forwards: admission, chunked prefill under a token budget, decode of every running request,
+retirement; ``king_v10/bundle_v9/slots.py:225-288`` runs inside such a loop).
+
+``submit(prompt, max_new_tokens, stop)`` queues a request; each ``step()`` either prefills newly admitted requests
+(up to ``prefill_tokens`` prompt tokens per step; a prompt longer than the budget is prefilled in chunks over
+several steps, every chunk attending to its cached prefix) or decodes one token for every running request (at most
+``max_running``, one batch, CUDA-graph bucketed by the engine).  Prefill has priority, as in the reference's
+disaggregated prefill role; finished requests release their KV pages at once.  Greedy sampling, or temperature /
+top-k sampling with a per-request seed.  On several ranks every rank runs the same scheduler on the same
+submissions (SPMD), so all ranks take the same steps.
+"""
+from __future__ import annotations
+
+from collections import deque
+from dataclasses import dataclass, field
+from typing import Deque, Dict, List, Optional, Sequence
+
+import torch
+
+from .engine import Engine, Request
+
+
+@dataclass
+class Job:
+    jid: int
+    prompt: List[int]
+    max_new_tokens: int
+    stop: Sequence[int] = ()
+    temperature: float = 0.0
+    top_k: int = 0
+    seed: int = 0
+    req: Optional[Request] = None
+    out: List[int] = field(default_factory=list)
+    pending: Optional[int] = None          # sampled token not yet fed to the model
+    done: bool = False
+
+    def sample(self, logits: torch.Tensor) -> int:
+        if self.temperature <= 0.0:
+            return int(torch.argmax(logits.float()))
+        lg = logits.float().cpu() / self.temperature
+        if self.top_k > 0:
+            v, i = torch.topk(lg, min(self.top_k, lg.numel()))
+            lg = torch.full_like(lg, float("-inf")).scatter_(0, i, v)
+        g = torch.Generator().manual_seed(self.seed * 1000003 + len(self.out))
+        return int(torch.multinomial(torch.softmax(lg, -1), 1, generator=g))
+
+
+class Scheduler:
+    def __init__(self, engine: Engine, max_running: int = 256, prefill_tokens: int = 32768):
+        self.eng = engine
+        self.max_running = max_running
+        self.prefill_tokens = prefill_tokens
+        self.waiting: Deque[Job] = deque()
+        self.prefilling: List[Job] = []        # admitted, prompt partly cached (chunked prefill)
+        self.running: List[Job] = []
+        self.finished: Dict[int, Job] = {}
+        self._next = 0
+        self.steps = {"prefill": 0, "decode": 0}
+
+    def submit(self, prompt: Sequence[int], max_new_tokens: int, stop: Sequence[int] = (), temperature: float = 0.0,
+               top_k: int = 0, seed: int = 0) -> int:
+        j = Job(self._next, list(prompt), max_new_tokens, tuple(stop), temperature, top_k, seed)
+        self._next += 1
+        self.waiting.append(j)
+        return j.jid
+
+    def idle(self) -> bool:
+        return not (self.waiting or self.prefilling or self.running)
+
+    def _finish(self, j: Job):
+        j.done = True
+        self.eng.release(j.req)
+        self.finished[j.jid] = j
+
+    def _take(self, j: Job, tok: int):
+        """Record a sampled token; retire the job when it is complete."""
+        j.out.append(tok)
+        if len(j.out) >= j.max_new_tokens or tok in j.stop:
+            self._finish(j)
+        else:
+            j.pending = tok
+            self.running.append(j)
+
+    def step(self) -> None:
+        budget = self.prefill_tokens
+        batch: List[Job] = []
+        counts: List[int] = []
+        # continue chunked prefills first, then admit new requests while the token budget and batch size allow
+        for j in list(self.prefilling):
+            if budget <= 0:
+                break
+            n = min(budget, j.req.seq_len - j.req.n_cached)
+            batch.append(j)
+            counts.append(n)
+            budget -= n
+        while self.waiting and budget > 0 and len(self.running) + len(self.prefilling) + 1 <= self.max_running:
+            j = self.waiting.popleft()
+            j.req = self.eng.add_request(j.prompt)
+            self.prefilling.append(j)
+            n = min(budget, len(j.prompt))
+            batch.append(j)
+            counts.append(n)
+            budget -= n
+        if batch:
+            self.steps["prefill"] += 1
+            whole = all(j.req.n_cached == 0 and n == len(j.prompt) for j, n in zip(batch, counts))
+            if whole:
+                logits = self.eng.prefill([j.req for j in batch])
+            else:
+                if self.eng.cfg.late_layer_start >= 0:
+                    for j in batch:
+                        if j.req.n_cached == 0:
+                            j.req.late_from = max(0, len(j.prompt) - self.eng.cfg.late_replay)
+                logits = self.eng._prefill_rows([j.req for j in batch], counts)
+            for j, row in zip(batch, logits):
+                if j.req.n_cached == j.req.seq_len:             # prompt complete: first output token
+                    self.prefilling.remove(j)
+                    self._take(j, j.sample(row))
+            return
+        if not self.running:
+            return
+        self.steps["decode"] += 1
+        run, self.running = self.running, []
+        logits = self.eng.decode([j.req for j in run], [j.pending for j in run])
+        for j, row in zip(run, logits):
+            self._take(j, j.sample(row))
+
+    def run(self) -> Dict[int, List[int]]:
+        """Step until every submitted job finished; returns {job id: output tokens}."""
+        while not self.idle():
+            self.step()
+        return {jid: j.out for jid, j in self.finished.items()}
