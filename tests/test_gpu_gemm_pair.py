@@ -235,7 +235,7 @@ def test_gather_fp8_rows_matches_gather_quantise():
 @pytest.mark.parametrize("H", [64, 32])
 def test_indexer_logits_fp8(H):
     """Block-scaled fp8 indexer logits (keys / queries in e4m3 with 1x128 UE8M0 scales) against the fp32 oracle of
-    the same fp8-rounded inputs."""
+    the same fp8-rounded inputs, on the causal entries."""
     from carbon_b200.ops.quant import quant_act
     from carbon_b200.ref import ops as R
 
@@ -251,6 +251,5 @@ def test_indexer_logits_fp8(H):
     kf, qf = R.fake_quant_fp8_rows(k.float()), R.fake_quant_fp8_rows(q.float())
     ref = R.indexer_logits(qf, kf, w)
     causal = torch.arange(L)[None, :] <= torch.arange(Tq)[:, None]
-    got = out[:, :L].cpu()
-    assert torch.isinf(got[~causal]).all() and (got[~causal] < 0).all()
+    got = out[:, :L].cpu()          # tiles wholly above the diagonal are skipped (the top-k reads causal keys only)
     assert ((got[causal] - ref[causal]).norm() / ref[causal].norm()).item() < 1e-3
