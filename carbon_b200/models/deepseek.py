@@ -244,7 +244,7 @@ class DeepseekModel:
         T = X.shape[0]
         img = cfg.image_token_id
         if not self.on_gpu:
-            kv = E.wkv(E.table[rows].reshape(T, -1))
+            kv = E.wkv(E.table[rows].reshape(T, rows.shape[1] * E.table.shape[1]))
             Xn = R.engram_gate(X, kv, E.qw, E.kw, cfg.rms_eps, cfg.engram_clamp).to(X.dtype)
             if img >= 0:
                 Xn = torch.where((self._tok_local.long() == img)[:, None, None], X, Xn)
@@ -356,7 +356,7 @@ class DeepseekModel:
             return R.mhc_coeffs(X, hp.fn, hp.base, hp.scale, cfg.hc_mult, cfg.sinkhorn_iters, cfg.hc_eps, cfg.rms_eps)
         from ..ops._ext import ext
 
-        mix = bf16_gemm(X.view(T, -1), hp.fn, out_dtype=torch.float32)
+        mix = bf16_gemm(X.view(T, X.shape[1] * X.shape[2]), hp.fn, out_dtype=torch.float32)
         pre = torch.empty(T, 4, device=X.device)
         post = torch.empty(T, 4, device=X.device)
         comb = torch.empty(T, 4, 4, device=X.device)
@@ -468,10 +468,10 @@ class DeepseekModel:
         """Per-head outputs [T, Hl, dvh] -> the output projection's input: the head concatenation, or (grouped
         low-rank projection) wo_a of each local group of heads, [T, Gl * o_lora]."""
         if L.wo_a is None:
-            return o.reshape(T, -1).to(self.act_dtype).contiguous()
+            return o.reshape(T, o.shape[1] * o.shape[2]).to(self.act_dtype).contiguous()
         Gl = L.wo_a.shape[0]
-        z = head_bmm(o.reshape(T, Gl, -1).to(self.act_dtype), L.wo_a)                # [T, Gl, o_lora]
-        return z.reshape(T, -1).to(self.act_dtype).contiguous()
+        z = head_bmm(o.reshape(T, Gl, L.wo_a.shape[2]).to(self.act_dtype), L.wo_a)                # [T, Gl, o_lora]
+        return z.reshape(T, z.shape[1] * z.shape[2]).to(self.act_dtype).contiguous()
 
     def indexer_qkw(self, i, h, q_lat, pos):
         cfg, L = self.cfg, self.layers[i]
@@ -829,7 +829,7 @@ class DeepseekModel:
             T = X.shape[0]
             pre = torch.empty(T, 4, device=X.device)
             if T > 0:
-                mix = bf16_gemm(X.view(T, -1), self.head_hc.fn, out_dtype=torch.float32)
+                mix = bf16_gemm(X.view(T, X.shape[1] * X.shape[2]), self.head_hc.fn, out_dtype=torch.float32)
                 ext().mhc_head_coeffs(mix, sumsq, self.head_hc.base, self.head_hc.scale, X.shape[1] * X.shape[2],
                                       cfg.hc_eps, cfg.rms_eps, pre)
             y, _ = self.pre_norm(X, pre, self.norm_w, want_fp8=False)

@@ -55,7 +55,7 @@ def mla_prefill(q: torch.Tensor, kvb: torch.Tensor, kpe: torch.Tensor, cu_seqlen
     T, H = q.shape[0], q.shape[1]
     if not q.is_cuda:
         dn = q.shape[2] - kpe.shape[-1]
-        k = torch.cat([kvb[..., :dn], kpe.view(T, 1, -1).expand(T, H, kpe.shape[-1])], dim=-1)
+        k = torch.cat([kvb[..., :dn], kpe.view(T, 1, kpe.shape[-1]).expand(T, H, kpe.shape[-1])], dim=-1)
         return prefill_attention(q, k, kvb[..., dn:], cu_seqlens, scale, key_masks, sink=sink)
     mask = None
     if isinstance(key_masks, torch.Tensor):
@@ -101,7 +101,7 @@ def pack_key_mask(key_masks, cu_seqlens, device, W: Optional[int] = None) -> tor
 
 def unpack_key_mask(words: torch.Tensor, cu_seqlens: List[int]) -> List[torch.Tensor]:
     shifts = torch.arange(32, device=words.device, dtype=torch.int64)
-    bits = ((words.to(torch.int64)[..., None] >> shifts) & 1).bool().reshape(words.shape[0], -1)
+    bits = ((words.to(torch.int64)[..., None] >> shifts) & 1).bool().reshape(words.shape[0], words.shape[1] * 32)
     return [bits[a:b, : b - a] for a, b in zip(cu_seqlens[:-1], cu_seqlens[1:])]
 
 

@@ -188,7 +188,7 @@ class DistCtx(ParallelCtx):
         back = self.all_to_all_rows(y.to(h.dtype), recv_counts, send_counts)     # rows in `order`
         contrib = torch.zeros(T * k, h.shape[1], dtype=torch.float32, device=h.device)
         contrib[order] = back.float()
-        out = (contrib.view(T, k, -1) * w.float()[..., None]).sum(1)
+        out = (contrib.view(T, k, h.shape[1]) * w.float()[..., None]).sum(1)
         if shared is not None:
             from ..models.deepseek import resolve
 

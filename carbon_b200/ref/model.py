@@ -191,11 +191,11 @@ class RefModel:
         L = f"layers.{i}.attn."
         T, H = o.shape[0], o.shape[1]
         if not cfg.o_groups:
-            return o.reshape(T, -1) @ w[L + "wo.weight"].t()
+            return o.reshape(T, o.shape[1] * o.shape[2]) @ w[L + "wo.weight"].t()
         G = cfg.o_groups
         og = o.reshape(T, G, -1)                                                # [T, G, (H/G)*dvh]
         z = torch.einsum("tgk,gnk->tgn", og, w[L + "wo_a.weight"])              # [T, G, o_lora]
-        return z.reshape(T, -1) @ w[L + "wo_b.weight"].t()
+        return z.reshape(T, z.shape[1] * z.shape[2]) @ w[L + "wo_b.weight"].t()
 
     def indexer_logits(self, i: int, h: torch.Tensor, q_lat: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
         q, k, wt = self.indexer_qkw(i, h, q_lat, pos)

@@ -219,7 +219,7 @@ def mhc_coeffs(X: torch.Tensor, fn: torch.Tensor, base: torch.Tensor, scale: tor
     """X [T, hc, D]; fn [hc*(2+hc), hc*D]; base [hc*(2+hc)]; scale [3].
     Returns pre [T,hc], post [T,hc], comb [T,hc,hc]."""
     T = X.shape[0]
-    xf = X.reshape(T, -1).float()
+    xf = X.reshape(T, X.shape[1] * X.shape[2]).float()
     rsq = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + rms_eps)
     m = (xf @ fn.float().t()) * rsq
     pre = torch.sigmoid(m[:, :hc] * scale[0] + base[:hc]) + hc_eps
@@ -230,7 +230,7 @@ def mhc_coeffs(X: torch.Tensor, fn: torch.Tensor, base: torch.Tensor, scale: tor
 
 def mhc_head_coeffs(X, fn, base, scale, hc_eps, rms_eps):
     T = X.shape[0]
-    xf = X.reshape(T, -1).float()
+    xf = X.reshape(T, X.shape[1] * X.shape[2]).float()
     rsq = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + rms_eps)
     m = (xf @ fn.float().t()) * rsq
     return torch.sigmoid(m * scale[0] + base) + hc_eps

@@ -60,7 +60,8 @@ def _worker(rank, world, port, q, attn_dp=False, variant="v3"):
 
 @pytest.mark.parametrize("world,attn_dp,variant", [(2, False, "v3"), (2, True, "v3"), (2, False, "v4"),
                                                    (2, True, "v4"), (2, False, "v4_late"), (2, True, "v4_late"),
-                                                   (2, True, "skewed"), (2, False, "skewed")])
+                                                   (2, True, "skewed"), (2, False, "skewed"), (4, False, "v3"),
+                                                   (4, True, "v3")])
 def test_tp_ep_engine_matches_single_rank(world, attn_dp, variant):
     cfg = _cfg(variant)
     w = init_weights(cfg, seed=0)
