@@ -43,3 +43,57 @@ def test_scheduler_stop_token_and_sampling():
     out = sch.run()
     assert out[a] == greedy[:greedy.index(greedy[2]) + 1]
     assert out[b] == out[c] and len(out[b]) == 8                # seeded sampling is reproducible
+
+
+def _sched_worker(rank, world, port, q):
+    import os
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from carbon_b200.parallel.dist import DistCtx
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    try:
+        cfg = tiny_config()
+        eng = Engine(cfg, "cpu", source=WeightSource(cfg, state=init_weights(cfg, seed=0)), num_pages=32,
+                     page_size=16, pctx=DistCtx(rank, world))
+        g = torch.Generator().manual_seed(5)
+        prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (70, 12, 33)]
+        sch = Scheduler(eng, max_running=2, prefill_tokens=40)
+        ids = [sch.submit(p, 5) for p in prompts]
+        out = sch.run()
+        q.put((rank, [out[i] for i in ids]))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_scheduler_spmd_two_ranks():
+    """Every rank runs the same scheduler on the same submissions (TP attention + EP MoE over gloo): the ranks take
+    the same steps and produce the single-rank tokens."""
+    import socket
+
+    import torch.multiprocessing as mp
+
+    cfg = tiny_config()
+    g = torch.Generator().manual_seed(5)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (70, 12, 33)]
+    ref = Engine(cfg, "cpu", source=WeightSource(cfg, state=init_weights(cfg, seed=0)), num_pages=32, page_size=16)
+    want = [ref.generate([p], 5)[0] for p in prompts]
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_sched_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(2)]
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, outs in res:
+        assert outs == want, rank
