@@ -155,7 +155,9 @@ class Engine:
     def prefill_chunked(self, reqs: List[Request], chunk: int) -> torch.Tensor:
         """Chunked prefill: each step runs at most ``chunk`` uncached prompt tokens per request, every token attending
         to its request's cached keys (the reference bounds a prefill step at 131,072 tokens, 32,768 per rank).
-        Returns logits [B, V] of each request's last prompt token."""
+        Returns logits [B, V] of each request's last prompt token.  Every row of a step carries its own key-slot
+        list, so a step's metadata is chunk x context int32 (e.g. 8,192 rows over a 32k context: 1 GB); size
+        ``chunk`` to the context length."""
         if self.cfg.late_layer_start >= 0:
             for r in reqs:                      # the replayed tail is fixed by the whole prompt
                 r.late_from = max(0, r.seq_len - self.cfg.late_replay)
