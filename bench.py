@@ -28,7 +28,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "prefill tok/s & decode out tok/s (8×B200, max over ranks); p50 TPOT; roofline %"
-BASELINE_VALUE = None  # BASELINE.md publishes no end-to-end number for this metric
+BASELINE_VALUE = None  # the reference publishes no end-to-end number for this metric
 
 
 def parse():

@@ -262,7 +262,7 @@ def tiny_v4_config() -> ModelConfig:
 
 
 def deepseek_v4_config() -> ModelConfig:
-    """DeepSeek-V4.1-Flash-shaped model (the reference's target): 40 layers, hidden 5120, 64 heads of
+    """DeepSeek-V4.1-Flash-shaped model (the reference's target model): 40 layers, hidden 5120, 64 heads of
     latent MQA over a 512-dim latent (64 RoPE dims), q_lora 1280, 8 output groups with o_lora 1024, window 128,
     indexer 32 heads x 128 top-512 on source layers 2, 8, 14, 384 experts top-6 (intermediate 2304, sqrt-softplus
     router), mHC 4 streams, Engram on layers 1 and 14 (24 hash columns of 256-dim rows).  The compressed KV pool is
