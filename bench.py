@@ -1,9 +1,9 @@
-"""Serving benchmark on BASELINE config 5 (full-size DeepSeek-V3/V4-class model, fp8 block-scaled, random init).
+"""Serving benchmark on the full-size model ( DeepSeek-V3/V4-class model, fp8 block-scaled, random init).
 
     python bench.py --gpus N --steps K --warmup W            # our engine (default N=1)
     python bench.py --impl reference ...                     # the reference's own build (see --impl reference)
 
-Per GPU (weak scaling; 8 GPUs = the BASELINE config): prefill 4 prompts × 4096 uniform-random token ids per step,
+Per GPU (weak scaling; 8 GPUs = the headline configuration): prefill 4 prompts × 4096 uniform-random token ids per step,
 decode a batch of 32 requests at context 4096 per step (global 32 prompts / batch 256 at N=8).  Timing: W untimed
 warm-up steps, then K steps bracketed by barrier + synchronize, CUDA events on the launching stream, max over
 ranks.  The weights (>100 GB) are far larger than L2, so every step streams them from HBM (no L2 flush needed).
@@ -49,7 +49,7 @@ def parse():
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                     help="multi-GPU data movement: our NVLink kernels (fused) or the NCCL baseline")
     ap.add_argument("--attn", default="tp", choices=["tp", "dp"],
-                    help="attention parallelism for N>1: tensor-parallel over heads (the BASELINE config) or "
+                    help="attention parallelism for N>1: tensor-parallel over heads (the headline configuration) or "
                          "data-parallel over each rank's own sequences")
     return ap.parse_args()
 

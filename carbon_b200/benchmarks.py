@@ -1,4 +1,4 @@
-"""Op-level benchmarks for the BASELINE configs, timed on the device with CUDA events and reported against the
+"""Op-level benchmarks (attention, mHC + GEMM, MoE, GEMM, decode attention), timed on the device with CUDA events and reported against the
 measured roofline (``MEASURED_PEAKS.json`` when present: ``bf16_tflops``, ``hbm_gbs``).
 
     python -m carbon_b200.benchmarks attn  [--batch 4 --seq 8192 --heads 128 --dsa]   # config 2

@@ -3,7 +3,7 @@
 One implementation runs on two kinds of device tensors:
 
 * CPU fp32 — every op resolves to the oracle math in ``carbon_b200.ref``; used to test the engine logic (paged
-  latent cache, absorbed decode, batching) against the naive full-recompute oracle.
+  latent cache, absorbed decode, batching) against the naive full-recompute oracle (the tiny CPU model).
 * CUDA (B200) — bf16 activations, block-scaled fp8 weights (128×128 UE8M0) and the sm_100a kernels in
   ``carbon_b200._C``.
 

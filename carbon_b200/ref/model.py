@@ -1,4 +1,4 @@
-"""CPU fp32 oracle of the whole model (BASELINE config 1 and the source of truth for every GPU path).
+"""CPU fp32 oracle of the whole model (the tiny CPU model's reference and the source of truth for every GPU path).
 
 The model is a DeepSeek-V3/V4-style decoder:
 

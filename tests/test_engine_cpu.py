@@ -1,4 +1,4 @@
-"""the tiny model served by the engine (paged latent cache, absorbed decode, DSA top-k) matches
+"""The tiny model served by the engine (paged latent cache, absorbed decode, DSA top-k) matches
 the naive full-recompute fp32 oracle within 1e-4 on every prefill and greedy-decode step."""
 import torch
 

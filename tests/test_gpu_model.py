@@ -244,7 +244,7 @@ def test_v4_late_replay_vs_oracle():
 
 
 def test_fp8_indexer_model_vs_oracle():
-    """The model with the fp8 e4m3 indexer (BASELINE config 5's precision): prefill selects keys with block-scaled
+    """The model with the fp8 e4m3 indexer (DeepSeek-V3.2's indexer precision): prefill selects keys with block-scaled
     fp8 logits, the oracle with fp32 logits of the same rounded inputs; a decode step agrees with the prefill of the
     longer prompt (decode's bf16 kernel sees the same rounded values)."""
     # against the oracle with top-256 of 300 keys (few near-tie selection flips between bf16 and fp32 activations)
