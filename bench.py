@@ -1,4 +1,4 @@
-"""Serving benchmark on the full-size model ( DeepSeek-V3/V4-class model, fp8 block-scaled, random init).
+"""Serving benchmark on the full-size DeepSeek-V3/V4-class model (fp8 block-scaled, random init).
 
     python bench.py --gpus N --steps K --warmup W            # our engine (default N=1)
     python bench.py --impl reference ...                     # the reference's own build (see --impl reference)
