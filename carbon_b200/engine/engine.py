@@ -47,6 +47,38 @@ def _meta_ext():
     return ext() if available() else None
 
 
+class PinnedStager:
+    """Reusable pinned host buffers for the per-step host -> device copies (token ids, positions, slots), so those
+    copies are asynchronous DMA from page-locked memory.  Each key alternates between two buffers; a buffer is
+    refilled only after the event recorded behind its last copy has completed.  CPU engines pass tensors through."""
+
+    def __init__(self, device):
+        self.device = device
+        self.bufs: Dict[str, list] = {}
+        self.turn: Dict[str, int] = {}
+
+    def to_device(self, key: str, t: torch.Tensor) -> torch.Tensor:
+        if self.device.type != "cuda":
+            return t
+        slots = self.bufs.setdefault(key, [None, None])
+        i = self.turn.get(key, 0)
+        self.turn[key] = i ^ 1
+        n = t.numel()
+        cur = slots[i]
+        if cur is not None:
+            cur[1].synchronize()                 # the copy that last read this buffer has finished
+        if cur is None or cur[0].numel() < n or cur[0].dtype != t.dtype:
+            cur = [torch.empty(max(n, 4096), dtype=t.dtype, pin_memory=True), None]
+            slots[i] = cur
+        view = cur[0][:n].view(t.shape)
+        view.copy_(t)
+        out = view.to(self.device, non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        cur[1] = ev
+        return out
+
+
 def decode_metadata(page_tables, seq_lens, page_size, pad_to, min_lmax=1):
     e = _meta_ext()
     if e is not None:
@@ -102,6 +134,7 @@ class Engine:
         from ..utils.metrics import Metrics
 
         self.metrics = Metrics()       # device-timed steps: summary(), json_line(), prometheus()
+        self.stager = PinnedStager(self.device)
 
     # -- request lifecycle -------------------------------------------------------------------------------------------
     def add_request(self, prompt: Sequence[int]) -> Request:
@@ -141,9 +174,10 @@ class Engine:
         for n in lens:
             cu.append(cu[-1] + n)
         rows = torch.tensor([c - 1 for c in cu[1:]], dtype=torch.int32)
-        fb = ForwardBatch(ids=torch.tensor(ids, dtype=torch.int32).to(dev, non_blocking=True),
-                          pos=pos.to(dev, non_blocking=True), out_loc=out_loc.to(dev, non_blocking=True),
-                          is_prefill=True, cu_seqlens=cu, logits_rows=rows.to(dev, non_blocking=True),
+        st = self.stager
+        fb = ForwardBatch(ids=st.to_device("ids", torch.tensor(ids, dtype=torch.int32)),
+                          pos=st.to_device("pos", pos), out_loc=st.to_device("loc", out_loc),
+                          is_prefill=True, cu_seqlens=cu, logits_rows=st.to_device("rows", rows),
                           bounds=self._bounds(lens))
         with self.metrics.step("prefill", sum(lens), len(reqs)):
             logits = self.model.forward(fb, self.cache)
@@ -213,15 +247,17 @@ class Engine:
         ids[:B] = torch.tensor([r.out[-1] for r in reqs], dtype=torch.int32)
         late = torch.zeros(bucket, dtype=torch.int32)
         late[:B] = torch.tensor([r.late_from for r in reqs], dtype=torch.int32)
+        st = self.stager
+        ids, pos, out_loc = st.to_device("d_ids", ids), st.to_device("d_pos", pos), st.to_device("d_loc", out_loc)
+        key_slots, n_keys = st.to_device("d_keys", key_slots), st.to_device("d_nk", n_keys)
+        late = st.to_device("d_late", late)
         with self.metrics.step("decode", B, B):
             if self.cuda_graphs and bucket is not None:
                 g = self._graph(bucket, key_slots.shape[1])
                 logits = g.run(ids, pos, out_loc, key_slots, n_keys, late)[:B]
             else:
-                dev = self.device
-                fb = ForwardBatch(ids=ids.to(dev), pos=pos.to(dev), out_loc=out_loc.to(dev), is_prefill=False,
-                                  key_slots=key_slots.to(dev), n_keys=n_keys.to(dev),
-                                  bounds=self._bounds([1] * bucket), late_from=late.to(dev))
+                fb = ForwardBatch(ids=ids, pos=pos, out_loc=out_loc, is_prefill=False, key_slots=key_slots,
+                                  n_keys=n_keys, bounds=self._bounds([1] * bucket), late_from=late)
                 logits = self.model.forward(fb, self.cache)[:B]
         for r in reqs:
             r.n_cached = r.seq_len
