@@ -10,9 +10,9 @@ from carbon_b200.ref import ops as R
 
 def test_sinkhorn_is_doubly_stochastic_and_mhc_ranges():
     g = torch.Generator().manual_seed(0)
-    c = R.sinkhorn(torch.randn(64, 4, 4, generator=g) * 3, 20, 1e-6)
+    c = R.sinkhorn(torch.randn(64, 4, 4, generator=g), 20, 1e-6)      # unit-scale logits, as mHC produces
     assert torch.allclose(c.sum(-2), torch.ones(64, 4), atol=1e-4)     # the last pass normalises columns exactly
-    assert torch.allclose(c.sum(-1), torch.ones(64, 4), atol=1e-2)     # rows converge to within 1 % in 20 passes
+    assert torch.allclose(c.sum(-1), torch.ones(64, 4), atol=1e-3)     # rows converge within 20 passes
     assert (c > 0).all()
     X = torch.randn(16, 4, 256, generator=g)
     fn = torch.randn(24, 4 * 256, generator=g) * 0.02
