@@ -116,7 +116,8 @@ def prefill_metadata(page_tables, starts, lens, page_size):
 class Engine:
     def __init__(self, cfg: ModelConfig, device="cpu", source: Optional[WeightSource] = None, num_pages: int = 256,
                  page_size: int = 64, model: Optional[DeepseekModel] = None, cuda_graphs: bool = False,
-                 graph_buckets: Sequence[int] = (1, 2, 4, 8, 16, 32, 64, 128, 256), pctx=None, fp8: bool = True):
+                 graph_buckets: Sequence[int] = (1, 2, 4, 8, 16, 32, 64, 128, 256), pctx=None, fp8: bool = True,
+                 prefix_cache: bool = False):
         self.cfg = cfg
         self.device = torch.device(device)
         self.model = model if model is not None else DeepseekModel(cfg, source or WeightSource(cfg), device,
@@ -135,17 +136,35 @@ class Engine:
 
         self.metrics = Metrics()       # device-timed steps: summary(), json_line(), prometheus()
         self.stager = PinnedStager(self.device)
+        # prefix reuse of full prompt pages (off with bounded late-layer replay: the late layers hold KV only for
+        # each prompt's own replayed tail)
+        self.prefix = None
+        if prefix_cache and cfg.late_layer_start < 0:
+            from .prefix_cache import PrefixCache
+
+            self.prefix = PrefixCache(self.cache.alloc, page_size)
 
     # -- request lifecycle -------------------------------------------------------------------------------------------
     def add_request(self, prompt: Sequence[int]) -> Request:
         r = Request(self._next_id, list(int(t) for t in prompt))
         self._next_id += 1
+        if self.prefix is not None:
+            r.pages = self.prefix.match(r.prompt)          # shared pages of the longest cached prefix
+            r.n_cached = len(r.pages) * self.page_size
         return r
 
     def _ensure_pages(self, r: Request, n_tokens: int):
         need = (n_tokens + self.page_size - 1) // self.page_size - len(r.pages)
         if need > 0:
+            if self.prefix is not None and self.cache.alloc.num_free() < need:
+                self.prefix.evict(need - self.cache.alloc.num_free())    # least recently used prefixes first
             r.pages += list(self.cache.alloc.alloc(need))
+
+    def _register_prefix(self, reqs: List[Request]) -> None:
+        if self.prefix is not None:
+            for r in reqs:
+                if r.n_cached >= len(r.prompt):
+                    self.prefix.insert(r.prompt, r.pages)
 
     def release(self, r: Request):
         if r.pages:
@@ -184,6 +203,7 @@ class Engine:
         for r, n in zip(reqs, lens):
             r.n_cached += n
         self.stats["prefill_tokens"] += sum(lens)
+        self._register_prefix(reqs)
         return logits
 
     def prefill_chunked(self, reqs: List[Request], chunk: int) -> torch.Tensor:
@@ -232,6 +252,7 @@ class Engine:
         for r, n in zip(reqs, counts):
             r.n_cached += n
         self.stats["prefill_tokens"] += m
+        self._register_prefix(reqs)
         return logits[torch.tensor(last, dtype=torch.long, device=logits.device)]
 
     def decode(self, reqs: List[Request], next_tokens: Sequence[int]) -> torch.Tensor:

@@ -98,7 +98,7 @@ class Scheduler:
             j = self.waiting.popleft()
             j.req = self.eng.add_request(j.prompt)
             self.prefilling.append(j)
-            n = min(budget, len(j.prompt))
+            n = min(budget, j.req.seq_len - j.req.n_cached)     # a cached prefix (prefix reuse) is skipped
             batch.append(j)
             counts.append(n)
             budget -= n
