@@ -315,6 +315,8 @@ def main():
                     "h2d_bytes_per_step": P * S * 4, "d2h_bytes_per_step": d2h // max(args.steps, 1)},
             "gpu_launches": launches,
             "clocks": clk.summary(),
+            "roofline": roofline(cfg, world, args.prompts_per_gpu, S, args.decode_batch_per_gpu, ctx, pf_ms, dec_ms,
+                                 load_peaks()),
             "config": {"model": f"{args.config} ({cfg.n_layers} layers, hidden {cfg.hidden_size}, "
                                 f"{cfg.n_routed_experts} experts top-{cfg.n_activated_experts})",
                        "global_batch": P, "seq_len": S, "decode_batch": B, "context": ctx,
@@ -349,6 +351,62 @@ def heap_bytes(cfg, world, max_tokens, max_seq):
     gathers = 2 * 2 * max_tokens * (width * 2 + (max_seq // 32 + 1) * 4 + cfg.index_topk * 4)
     emb = (cfg.vocab_size // world + 1) * D * 2
     return int(rs + moe + gathers + emb + (1 << 30))
+
+
+def roofline(cfg, world: int, prompts_per_gpu: int, seq: int, decode_per_gpu: int, ctx: int, prefill_ms: float,
+             decode_ms: float, peak: dict) -> dict:
+    """Fraction of a hardware bound reached per GPU per step (estimates from the model shape).
+
+    Prefill (compute bound): the step's model FLOPs at the measured peaks (fp8 GEMMs at 2x the sustained bf16 rate,
+    attention and indexer at the sustained bf16 rate) divided by the measured step time.  Decode (memory bound):
+    the bytes a step must stream (expected distinct routed experts per rank under uniform routing, this rank's
+    attention / shared / dense weights, the selected latent rows and the indexer keys of its tokens) at the
+    measured HBM bandwidth, divided by the measured step time."""
+    D, H, L = cfg.hidden_size, cfg.n_heads, cfg.n_layers
+    dq, dv, r, dr = cfg.qk_head_dim, cfg.head_out_dim, cfg.kv_lora_rank, cfg.qk_rope_head_dim
+    dn = cfg.qk_nope_head_dim
+    E, k, I, ql = cfg.n_routed_experts, cfg.n_activated_experts, cfg.moe_intermediate, cfg.q_lora_rank
+    n_idx = sum(1 for l in range(L) if cfg.has_indexer(l))
+    n_moe = sum(1 for l in range(L) if cfg.is_moe_layer(l))
+    n_dense = L - n_moe
+    attn_w = D * ql + ql * H * dq + D * cfg.latent_dim + r * H * (dn + dv) + H * dv * D        # params / layer
+    idx_w = ql * cfg.index_n_heads * cfg.index_head_dim + D * cfg.index_head_dim + D * cfg.index_n_heads
+    expert = 3 * D * I
+    topk = cfg.index_topk if cfg.use_indexer else seq
+    avg_keys = sum(min(p + 1, topk) for p in range(seq)) / seq
+    avg_all = (seq + 1) / 2
+    tok = prompts_per_gpu * seq
+    fp8_flops = tok * 2 * (L * attn_w + n_moe * (k + cfg.n_shared_experts) * expert + n_dense * 3 * D *
+                           cfg.dense_intermediate)
+    bf16_flops = tok * 2 * (L * H * (dq + dv) * avg_keys + n_idx * (idx_w + cfg.index_n_heads *
+                                                                    cfg.index_head_dim * avg_all))
+    bf16 = peak["bf16_tflops_sustained"] * 1e12
+    t_pf = fp8_flops / (2 * bf16) + bf16_flops / bf16
+    B_tot = decode_per_gpu * world
+    El = E // world
+    touched = El * (1 - (1 - 1 / E) ** (B_tot * k)) if E else 0
+    wbytes = n_moe * (touched * expert + cfg.n_shared_experts * expert) + L * attn_w / world + \
+        n_dense * 3 * D * cfg.dense_intermediate + n_idx * idx_w * 2
+    kv = decode_per_gpu * (L * min(ctx, topk) * cfg.latent_dim * 2 + n_idx * ctx * cfg.index_head_dim * 2)
+    t_dec = (wbytes + kv) / (peak["hbm_gbs"] * 1e9)
+    return {"prefill_frac": round(t_pf / (prefill_ms / 1e3), 3), "decode_frac": round(t_dec / (decode_ms / 1e3), 3),
+            "prefill_tflop_per_gpu_step": round((fp8_flops + bf16_flops) / 1e12, 1),
+            "decode_gb_per_gpu_step": round((wbytes + kv) / 1e9, 1),
+            "basis": "per GPU per step; prefill: model FLOPs at measured peaks (fp8 = 2x sustained bf16); decode: "
+                     "streamed bytes (expected routed experts touched, weights, selected KV rows, indexer keys) at "
+                     "measured HBM bandwidth"}
+
+
+def load_peaks() -> dict:
+    """Measured peaks of this pool (driver-written MEASURED_PEAKS.json); the pool's earlier measurement otherwise."""
+    p = os.path.join(os.path.dirname(os.path.abspath(__file__)), "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return {"bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", d["bf16_tflops"])),
+                "hbm_gbs": float(d["hbm_gbs"])}
+    except (OSError, KeyError, ValueError):
+        return {"bf16_tflops_sustained": 1400.0, "hbm_gbs": 6650.0}
 
 
 def max_over_ranks(v: float, world: int) -> float:

@@ -21,3 +21,25 @@ def test_engine_metrics():
     assert rec["rank"] == 0 and "decode" in rec["metrics"]
     prom = eng.metrics.prometheus()
     assert 'carbon_tokens_total{kind="prefill"} 44' in prom and 'carbon_tpot_ms{quantile="50"}' in prom
+
+
+def test_bench_roofline_estimate():
+    """The bench's roofline fractions: ~83 GFLOP per prefill token and ~440 GB per one-GPU decode step for the
+    full-size model (37B active parameters; ~160 of 256 experts touched per layer by 32 tokens x top-8)."""
+    import importlib.util
+    import os
+
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "bench.py")
+    spec = importlib.util.spec_from_file_location("carbon_bench", path)
+    b = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(b)
+    from carbon_b200.config import PRESETS
+
+    cfg = PRESETS["deepseek_v3"]()
+    peak = {"bf16_tflops_sustained": 1400.0, "hbm_gbs": 6500.0}
+    r1 = b.roofline(cfg, 1, 4, 4096, 32, 4096, 1200.0, 110.0, peak)
+    assert 70 < r1["prefill_tflop_per_gpu_step"] * 1e12 / (4 * 4096) / 1e9 < 95
+    assert 400 < r1["decode_gb_per_gpu_step"] < 480
+    assert 0 < r1["prefill_frac"] < 1 and 0 < r1["decode_frac"] < 1
+    r8 = b.roofline(cfg, 8, 4, 4096, 32, 4096, 1680.0, 74.0, peak)
+    assert r8["decode_gb_per_gpu_step"] < r1["decode_gb_per_gpu_step"] / 4          # 32 experts per rank
