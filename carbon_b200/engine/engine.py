@@ -117,7 +117,7 @@ class Engine:
     def __init__(self, cfg: ModelConfig, device="cpu", source: Optional[WeightSource] = None, num_pages: int = 256,
                  page_size: int = 64, model: Optional[DeepseekModel] = None, cuda_graphs: bool = False,
                  graph_buckets: Sequence[int] = (1, 2, 4, 8, 16, 32, 64, 128, 256), pctx=None, fp8: bool = True,
-                 prefix_cache: bool = False):
+                 prefix_cache: bool = False, record_expert_load: bool = False):
         self.cfg = cfg
         self.device = torch.device(device)
         self.model = model if model is not None else DeepseekModel(cfg, source or WeightSource(cfg), device,
@@ -138,6 +138,10 @@ class Engine:
         self.stager = PinnedStager(self.device)
         # prefix reuse of full prompt pages (off with bounded late-layer replay: the late layers hold KV only for
         # each prompt's own replayed tail)
+        if record_expert_load and cfg.n_routed_experts:
+            from ..parallel.placement import ExpertLoad
+
+            self.model.expert_load = ExpertLoad(cfg.n_routed_experts)
         self.prefix = None
         if prefix_cache and cfg.late_layer_start < 0:
             from .prefix_cache import PrefixCache
@@ -159,6 +163,18 @@ class Engine:
             if self.prefix is not None and self.cache.alloc.num_free() < need:
                 self.prefix.evict(need - self.cache.alloc.num_free())    # least recently used prefixes first
             r.pages += list(self.cache.alloc.alloc(need))
+
+    def rebalance_experts(self):
+        """Expert placement from the routing recorded while serving (``record_expert_load=True``): every MoE layer's
+        experts are relabelled and moved so each EP rank carries a similar load.  Captured decode graphs are dropped
+        (they hold the old weight tensors) and recaptured on the next decode.  All ranks call it together."""
+        from ..parallel import placement
+
+        if self.model.expert_load is None:
+            raise RuntimeError("construct the engine with record_expert_load=True")
+        out = placement.rebalance(self.model, self.model.expert_load)
+        self._graphs.clear()
+        return out
 
     def _register_prefix(self, reqs: List[Request]) -> None:
         if self.prefix is not None:

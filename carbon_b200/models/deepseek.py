@@ -151,6 +151,7 @@ class DeepseekModel:
         self.pctx = pctx if pctx is not None else ParallelCtx.single()
         self.fp8 = fp8
         self.trace = None          # set to a list to record (name, tensor) at sublayer boundaries (debugging)
+        self.expert_load = None    # placement.ExpertLoad: per-layer routing counts for expert rebalancing
         self._side = None          # side stream of the shared expert
         self._dsa = {}
         cfg.validate()
@@ -672,6 +673,8 @@ class DeepseekModel:
                                    tok=self._tok_local if L.gate_b_img is not None else None,
                                    img_id=cfg.image_token_id)
         self._tr(f"{i}.router_ids", ids)
+        if self.expert_load is not None:
+            self.expert_load.record_device(i, ids)
         shared = None
         if L.shared is not None:
             if self.on_gpu:

@@ -25,10 +25,30 @@ class ExpertLoad:
     def __init__(self, n_experts: int):
         self.E = n_experts
         self.counts: Dict[int, torch.Tensor] = {}
+        self.dev_counts: Dict[int, torch.Tensor] = {}
 
     def record(self, layer: int, ids: torch.Tensor) -> None:
         c = torch.bincount(ids.reshape(-1).long().cpu(), minlength=self.E)
         self.counts[layer] = self.counts.get(layer, torch.zeros(self.E, dtype=torch.long)) + c
+
+    def record_device(self, layer: int, ids: torch.Tensor) -> None:
+        """Accumulate on the router's device with a scatter-add: no host synchronisation, so it also runs inside
+        captured decode graphs (the counter exists from the first eager step on)."""
+        c = self.dev_counts.get(layer)
+        if c is None:
+            c = torch.zeros(self.E, dtype=torch.int64, device=ids.device)
+            self.dev_counts[layer] = c
+        flat = ids.reshape(-1).long()
+        c.index_add_(0, flat, torch.ones_like(flat))
+
+    def take(self, layer: int) -> torch.Tensor:
+        """This rank's counts of one layer since the last take (host and device records), then reset."""
+        out = self.counts.pop(layer, torch.zeros(self.E, dtype=torch.long)).clone()
+        c = self.dev_counts.get(layer)
+        if c is not None:
+            out += c.cpu()
+            c.zero_()
+        return out
 
 
 def plan(load: torch.Tensor, ep: int) -> torch.Tensor:
@@ -144,3 +164,28 @@ def redistribute(model, layer: int, perm: torch.Tensor) -> None:
         L.e_w1 = _exchange_experts(L.e_w1.contiguous(), perm, E, ep, rank, group)
         L.e_w3 = _exchange_experts(L.e_w3.contiguous(), perm, E, ep, rank, group)
         L.e_w2 = _exchange_experts(L.e_w2.contiguous(), perm, E, ep, rank, group)
+
+
+def rebalance(model, load: "ExpertLoad") -> Dict[int, tuple]:
+    """Plan and apply a balanced placement for every MoE layer from the routing recorded since the last call.  The
+    counts are summed over the EP ranks first, so every rank plans the same permutation; weights then move with
+    ``redistribute`` (``apply`` on one rank).  Returns {layer: (imbalance before, after)}."""
+    import torch.distributed as dist
+
+    pc = model.pctx
+    if model.n_weight_sets < model.cfg.n_layers:
+        raise RuntimeError("rebalance needs untied layers: tied layers share one expert set")
+    out = {}
+    for layer in range(model.cfg.n_layers):
+        if not model.layers[layer].moe:
+            continue
+        c = load.take(layer)
+        if pc.world > 1:
+            dev = model.device if dist.get_backend(getattr(pc, "group", None)) == "nccl" else torch.device("cpu")
+            t = c.to(dev)
+            dist.all_reduce(t, group=getattr(pc, "group", None))
+            c = t.cpu()
+        perm = plan(c, pc.ep)
+        out[layer] = (imbalance(c, pc.ep), imbalance(c, pc.ep, perm))
+        redistribute(model, layer, perm)
+    return out

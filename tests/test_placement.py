@@ -48,7 +48,7 @@ def _redistribute_worker(rank, world, port, q):
         cfg = tiny_config()
         w = init_weights(cfg, seed=0)
         e = Engine(cfg, "cpu", source=WeightSource(cfg, state=w), num_pages=16, page_size=16,
-                   pctx=DistCtx(rank, world))
+                   pctx=DistCtx(rank, world), record_expert_load=True)
         prompts = [torch.arange(40).tolist(), (torch.arange(30) * 7 % cfg.vocab_size).tolist()]
         ref, h_ref = e.generate(prompts, 5, return_logits=True)
         for layer in range(cfg.n_layers):
@@ -56,7 +56,14 @@ def _redistribute_worker(rank, world, port, q):
             placement.redistribute(e.model, layer, perm)
         out, h = e.generate(prompts, 5, return_logits=True)
         err = max(float((a - b).abs().max()) for a, b in zip(h, h_ref))
-        q.put((rank, out == ref, err))
+        same = out == ref
+        # the engine's own loop: routing recorded while serving, counts summed over ranks, one plan per layer
+        stats = e.rebalance_experts()
+        out2, h2 = e.generate(prompts, 5, return_logits=True)
+        err = max(err, max(float((a - b).abs().max()) for a, b in zip(h2, h_ref)))
+        same = same and out2 == ref and all(after <= before + 1e-6 for before, after in stats.values())
+        same = same and len(stats) == sum(1 for L in e.model.layers if L.moe)
+        q.put((rank, same, err))
     finally:
         dist.destroy_process_group()
 
@@ -83,3 +90,30 @@ def test_redistribute_across_ranks_is_output_preserving():
         assert p.exitcode == 0
     for rank, same, err in res:
         assert same and err < 1e-4, (rank, same, err)
+
+
+def test_expert_load_device_recorder_matches_bincount():
+    g = torch.Generator().manual_seed(3)
+    ids = torch.randint(0, 16, (37, 4), generator=g)
+    load = placement.ExpertLoad(16)
+    load.record_device(2, ids)
+    load.record_device(2, ids[:5])
+    load.record(2, ids[5:9])
+    want = torch.bincount(torch.cat([ids.reshape(-1), ids[:5].reshape(-1), ids[5:9].reshape(-1)]), minlength=16)
+    assert torch.equal(load.take(2), want)
+    assert int(load.take(2).sum()) == 0                                          # take() resets
+
+
+def test_engine_rebalance_single_rank_is_output_preserving():
+    cfg = tiny_config()
+    w = init_weights(cfg, seed=0)
+    prompts = [torch.arange(40).tolist(), (torch.arange(30) * 7 % cfg.vocab_size).tolist()]
+    e = Engine(cfg, "cpu", source=WeightSource(cfg, state=w), num_pages=16, page_size=16, record_expert_load=True)
+    ref, h_ref = e.generate(prompts, 5, return_logits=True)
+    counts = {i: c.clone() for i, c in e.model.expert_load.dev_counts.items()}
+    assert counts and all(int(c.sum()) > 0 for c in counts.values())
+    stats = e.rebalance_experts()
+    assert set(stats) == set(counts)
+    out, h = e.generate(prompts, 5, return_logits=True)
+    assert out == ref
+    assert max(float((a - b).abs().max()) for a, b in zip(h, h_ref)) < 1e-4
