@@ -117,7 +117,7 @@ class Engine:
     def __init__(self, cfg: ModelConfig, device="cpu", source: Optional[WeightSource] = None, num_pages: int = 256,
                  page_size: int = 64, model: Optional[DeepseekModel] = None, cuda_graphs: bool = False,
                  graph_buckets: Sequence[int] = (1, 2, 4, 8, 16, 32, 64, 128, 256), pctx=None, fp8: bool = True,
-                 prefix_cache: bool = False, record_expert_load: bool = False):
+                 prefix_cache: bool = False, record_expert_load: bool = False, balance_dp: bool = False):
         self.cfg = cfg
         self.device = torch.device(device)
         self.model = model if model is not None else DeepseekModel(cfg, source or WeightSource(cfg), device,
@@ -138,6 +138,8 @@ class Engine:
         self.stager = PinnedStager(self.device)
         # prefix reuse of full prompt pages (off with bounded late-layer replay: the late layers hold KV only for
         # each prompt's own replayed tail)
+        # DP attention: place prefill sequences and decode rows on ranks by a FLOP cost model instead of by count
+        self.balance_dp = balance_dp
         if record_expert_load and cfg.n_routed_experts:
             from ..parallel.placement import ExpertLoad
 
@@ -188,11 +190,27 @@ class Engine:
             r.pages = []
 
     # -- steps ---------------------------------------------------------------------------------------------------------
+    def _dp_balanced(self) -> bool:
+        pc = self.model.pctx
+        return self.balance_dp and pc.world > 1 and pc.attn_dp
+
     def prefill(self, reqs: List[Request]) -> torch.Tensor:
         """Run every request's uncached prompt tokens; returns logits [B, V] of each request's last token.  Requests
         with a cached prefix (chunked prefill, prefix reuse) continue through per-row attention over the cache."""
         if any(r.n_cached > 0 for r in reqs):
             return self._prefill_rows(reqs, [r.seq_len - r.n_cached for r in reqs])
+        if self._dp_balanced() and len(reqs) > 1:
+            from ..parallel.balance import plan_prefill
+
+            order, bounds, _ = plan_prefill(self.cfg, [r.seq_len for r in reqs], self.model.pctx.world)
+            logits = self._prefill_full([reqs[i] for i in order], bounds)
+            inv = [0] * len(order)
+            for j, i in enumerate(order):
+                inv[i] = j
+            return logits[torch.tensor(inv, dtype=torch.long, device=logits.device)]
+        return self._prefill_full(reqs, None)
+
+    def _prefill_full(self, reqs: List[Request], bounds: Optional[List[int]]) -> torch.Tensor:
         dev = self.device
         ids, starts, lens = [], [], []
         for r in reqs:
@@ -213,7 +231,7 @@ class Engine:
         fb = ForwardBatch(ids=st.to_device("ids", torch.tensor(ids, dtype=torch.int32)),
                           pos=st.to_device("pos", pos), out_loc=st.to_device("loc", out_loc),
                           is_prefill=True, cu_seqlens=cu, logits_rows=st.to_device("rows", rows),
-                          bounds=self._bounds(lens))
+                          bounds=bounds if bounds is not None else self._bounds(lens))
         with self.metrics.step("prefill", sum(lens), len(reqs)):
             logits = self.model.forward(fb, self.cache)
         for r, n in zip(reqs, lens):
@@ -273,6 +291,20 @@ class Engine:
 
     def decode(self, reqs: List[Request], next_tokens: Sequence[int]) -> torch.Tensor:
         """Append one token per request and run it; returns logits [B, V]."""
+        if self._dp_balanced() and len(reqs) > 1:
+            from ..parallel.balance import plan_rows, seq_cost
+
+            n = self._bucket(len(reqs)) if self.cuda_graphs else len(reqs)
+            n = n if n is not None else len(reqs)
+            perm = plan_rows([seq_cost(self.cfg, 1, r.seq_len) for r in reqs], self._bounds([1] * n))
+            logits = self._decode([reqs[i] for i in perm], [next_tokens[i] for i in perm])
+            inv = [0] * len(perm)
+            for j, i in enumerate(perm):
+                inv[i] = j
+            return logits[torch.tensor(inv, dtype=torch.long, device=logits.device)]
+        return self._decode(reqs, next_tokens)
+
+    def _decode(self, reqs: List[Request], next_tokens: Sequence[int]) -> torch.Tensor:
         B = len(reqs)
         for r, t in zip(reqs, next_tokens):
             r.out.append(int(t))

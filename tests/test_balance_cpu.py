@@ -1,0 +1,115 @@
+"""Cost-model balancing of DP attention ranks: the planner evens out skewed batches, and an engine that places its
+prefill sequences and decode rows by the plan serves exactly the same tokens as one that splits by count."""
+import socket
+
+import torch
+
+from carbon_b200.config import deepseek_v3_config, tiny_config
+from carbon_b200.parallel import balance
+from carbon_b200.parallel.dist import split_bounds
+
+
+def test_seq_cost_grows_with_context_and_respects_caps():
+    cfg = deepseek_v3_config()
+    # prefill cost is superlinear in length (attention / indexer pairs), decode cost grows with the context
+    assert balance.seq_cost(cfg, 8192) > 2.05 * balance.seq_cost(cfg, 4096)
+    assert balance.seq_cost(cfg, 1, 8192) > balance.seq_cost(cfg, 1, 1024)
+    assert balance._capped_pairs(0, 10, 0) == 55
+    assert balance._capped_pairs(0, 10, 4) == sum(min(p + 1, 4) for p in range(10))
+    assert balance._capped_pairs(5, 7, 6) == sum(min(p + 1, 6) for p in range(5, 12))
+
+
+def test_plan_prefill_beats_token_split_on_skewed_batch():
+    cfg = deepseek_v3_config()
+    lengths = [8192, 8192] + [1024] * 16                    # the token split puts both long prompts on rank 0
+    world = 2
+    order, bounds, load = balance.plan_prefill(cfg, lengths, world)
+    assert sorted(order) == list(range(len(lengths)))
+    assert bounds[0] == 0 and bounds[-1] == sum(lengths)
+    # each rank's tokens are whole sequences of the reordered batch
+    acc, cuts = 0, {0}
+    for i in order:
+        acc += lengths[i]
+        cuts.add(acc)
+    assert set(bounds) <= cuts
+    base = balance.split_costs(cfg, lengths, split_bounds(lengths, world))
+    assert balance.imbalance(load) < 1.01 < 1.1 < balance.imbalance(base)   # DSA caps attention: ~1.12
+    assert abs(sum(load) - sum(base)) / sum(base) < 1e-9
+
+
+def test_plan_rows_keeps_block_capacities():
+    g = torch.Generator().manual_seed(0)
+    ctx = torch.randint(16, 30000, (13,), generator=g).tolist()
+    cfg = deepseek_v3_config()
+    costs = [balance.seq_cost(cfg, 1, c) for c in ctx]
+    bounds = split_bounds([1] * 16, 4)                      # bucket 16 (3 padding rows) over 4 ranks
+    perm = balance.plan_rows(costs, bounds)
+    assert sorted(perm) == list(range(13))
+    per = [sum(costs[perm[j]] for j in range(bounds[r], min(bounds[r + 1], 13))) for r in range(4)]
+    naive = [sum(costs[j] for j in range(bounds[r], min(bounds[r + 1], 13))) for r in range(4)]
+    assert max(per) <= max(naive) + 1e-6
+
+
+def _prompts(cfg):
+    return [(torch.arange(90) * 5 % cfg.vocab_size).tolist(), (torch.arange(60) * 3 % cfg.vocab_size).tolist(),
+            list(range(1, 9)), list(range(20, 27)), list(range(40, 50)), list(range(60, 69))]
+
+
+def _worker(rank, world, port, q, balanced):
+    import os
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from carbon_b200.engine.engine import Engine
+    from carbon_b200.models.weights import WeightSource
+    from carbon_b200.parallel.dist import DistCtx
+    from carbon_b200.ref.model import init_weights
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    try:
+        cfg = tiny_config()
+        w = init_weights(cfg, seed=0)
+        e = Engine(cfg, device="cpu", source=WeightSource(cfg, state=w), num_pages=48, page_size=16,
+                   pctx=DistCtx(rank, world, attn_dp=True), balance_dp=balanced)
+        prompts = _prompts(cfg)
+        out, h = e.generate(prompts, 4, return_logits=True)
+        q.put((rank, balanced, out, [x.tolist() for x in h]))       # plain lists: no shared-memory handles
+    finally:
+        dist.destroy_process_group()
+
+
+def _run(balanced):
+    import torch.multiprocessing as mp
+
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, q, balanced)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = [q.get(timeout=300) for _ in range(2)]
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    return sorted(res, key=lambda x: x[0])
+
+
+def test_balanced_dp_engine_serves_the_same_tokens():
+    cfg = tiny_config()
+    lens = [len(p) for p in _prompts(cfg)]
+    # the plans differ from the count split, so the balanced run really reorders prefill and decode
+    assert balance.plan_prefill(cfg, lens, 2)[1] != split_bounds(lens, 2)
+    perm = balance.plan_rows([balance.seq_cost(cfg, 1, n + 1) for n in lens], split_bounds([1] * len(lens), 2))
+    assert perm != list(range(len(lens)))
+    plain = _run(False)
+    bal = _run(True)
+    for (r0, _, out0, h0), (r1, _, out1, h1) in zip(plain, bal):
+        assert out0 == out1, (r0, out0, out1)
+        for a, b in zip(h0, h1):
+            assert (torch.tensor(a) - torch.tensor(b)).abs().max() < 1e-3
