@@ -166,6 +166,17 @@ class Engine:
                 self.prefix.evict(need - self.cache.alloc.num_free())    # least recently used prefixes first
             r.pages += list(self.cache.alloc.alloc(need))
 
+    def check_device(self) -> None:
+        """Raise if a cross-rank kernel recorded an error (a bounded wait that ran out, a capacity overflow) in the
+        parallel context's status word.  Contexts without device-side exchanges have nothing to check."""
+        chk = getattr(self.model.pctx, "check", None)
+        code = chk() if chk is not None else 0
+        if code:
+            what = {1: "producer data never arrived", 2: "a pipeline stage was never released",
+                    3: "accumulator hand-off timed out", 4: "a peer rank's flag never arrived",
+                    5: "bad argument"}.get(code, "unknown")
+            raise RuntimeError(f"cross-rank kernel status {code}: {what}")
+
     def rebalance_experts(self):
         """Expert placement from the routing recorded while serving (``record_expert_load=True``): every MoE layer's
         experts are relabelled and moved so each EP rank carries a similar load.  Captured decode graphs are dropped

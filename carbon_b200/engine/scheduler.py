@@ -47,8 +47,15 @@ class Job:
 
 
 class Scheduler:
-    def __init__(self, engine: Engine, max_running: int = 256, prefill_tokens: int = 32768):
+    def __init__(self, engine: Engine, max_running: int = 256, prefill_tokens: int = 32768, heartbeat=None,
+                 watchdog=None, check_device: bool = False):
+        """heartbeat (``utils.health.Heartbeat``): checked before every step, so a dead peer stops this rank before
+        it launches work that would wait for it; watchdog (``utils.health.Watchdog``): a step that overruns its
+        limit raises ``StepStalled``; check_device: read the cross-rank kernels' status word after every step."""
         self.eng = engine
+        self.heartbeat = heartbeat
+        self.watchdog = watchdog
+        self.check_device = check_device
         self.max_running = max_running
         self.prefill_tokens = prefill_tokens
         self.waiting: Deque[Job] = deque()
@@ -83,6 +90,17 @@ class Scheduler:
             self.running.append(j)
 
     def step(self) -> None:
+        if self.heartbeat is not None:
+            self.heartbeat.check()
+        if self.watchdog is None:
+            self._step()
+        else:
+            with self.watchdog.step("scheduler step"):
+                self._step()
+        if self.check_device:
+            self.eng.check_device()
+
+    def _step(self) -> None:
         budget = self.prefill_tokens
         batch: List[Job] = []
         counts: List[int] = []
