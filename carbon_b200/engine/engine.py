@@ -159,11 +159,23 @@ class Engine:
             r.n_cached = len(r.pages) * self.page_size
         return r
 
+    def pages_for(self, r: Request, n_tokens: int) -> int:
+        """New KV pages request ``r`` needs to hold ``n_tokens`` tokens."""
+        return max(0, (n_tokens + self.page_size - 1) // self.page_size - len(r.pages))
+
+    def pages_available(self) -> int:
+        """Pages an allocation can get now: free pages plus cached prefix pages that only the prefix cache holds."""
+        a = self.cache.alloc
+        n = a.num_free()
+        if self.prefix is not None:
+            n += sum(1 for p in self.prefix.entries.values() if a.refcount(p) == 1)
+        return n
+
     def _ensure_pages(self, r: Request, n_tokens: int):
-        need = (n_tokens + self.page_size - 1) // self.page_size - len(r.pages)
+        need = self.pages_for(r, n_tokens)
         if need > 0:
-            if self.prefix is not None and self.cache.alloc.num_free() < need:
-                self.prefix.evict(need - self.cache.alloc.num_free())    # least recently used prefixes first
+            while self.prefix is not None and self.cache.alloc.num_free() < need and self.prefix.entries:
+                self.prefix.evict(1)             # least recently used prefixes first (shared ones free nothing)
             r.pages += list(self.cache.alloc.alloc(need))
 
     def check_device(self) -> None:

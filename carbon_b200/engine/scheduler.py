@@ -6,7 +6,10 @@ retirement; ``king_v10/bundle_v9/slots.py:225-288`` runs inside such a loop).
 (up to ``prefill_tokens`` prompt tokens per step; a prompt longer than the budget is prefilled in chunks over
 several steps, every chunk attending to its cached prefix) or decodes one token for every running request (at most
 ``max_running``, one batch, CUDA-graph bucketed by the engine).  Prefill has priority, as in the reference's
-disaggregated prefill role; finished requests release their KV pages at once.  Greedy sampling, or temperature /
+disaggregated prefill role; finished requests release their KV pages at once.  Admission waits for free KV pages
+(keeping one page of headroom per running request); when a decode step would run out of pages, the youngest
+requests are preempted by recompute: their pages are freed, they rejoin the queue first and, on readmission,
+prefill their prompt plus the tokens they already generated (a prefix-cache hit when enabled) and continue.  Greedy sampling, or temperature /
 top-k sampling with a per-request seed.  On several ranks every rank runs the same scheduler on the same
 submissions (SPMD), so all ranks take the same steps.
 """
@@ -34,6 +37,12 @@ class Job:
     out: List[int] = field(default_factory=list)
     pending: Optional[int] = None          # sampled token not yet fed to the model
     done: bool = False
+    admit: int = -1                        # admission order (preemption retracts the youngest first)
+
+    def tokens(self) -> List[int]:
+        """Tokens to prefill on (re)admission: the prompt, plus, after a preemption, every output token already fed
+        to the model (the last sampled one is still pending)."""
+        return self.prompt + self.out[:-1]
 
     def sample(self, logits: torch.Tensor) -> int:
         if self.temperature <= 0.0:
@@ -63,10 +72,16 @@ class Scheduler:
         self.running: List[Job] = []
         self.finished: Dict[int, Job] = {}
         self._next = 0
+        self._admits = 0
+        self.preemptions = 0
         self.steps = {"prefill": 0, "decode": 0}
 
     def submit(self, prompt: Sequence[int], max_new_tokens: int, stop: Sequence[int] = (), temperature: float = 0.0,
                top_k: int = 0, seed: int = 0) -> int:
+        cap = (self.eng.cache.alloc.num_pages() - 1) * self.eng.page_size       # page 0 is the graphs' scratch
+        if len(prompt) + max_new_tokens > cap:
+            raise ValueError(f"prompt + max_new_tokens = {len(prompt) + max_new_tokens} tokens exceed the KV cache "
+                             f"({cap} tokens)")
         j = Job(self._next, list(prompt), max_new_tokens, tuple(stop), temperature, top_k, seed)
         self._next += 1
         self.waiting.append(j)
@@ -100,47 +115,92 @@ class Scheduler:
         if self.check_device:
             self.eng.check_device()
 
+    def _retract(self, j: Job) -> None:
+        """Preempt by recompute: free the job's KV pages and queue it first; on readmission it prefills its prompt
+        and the tokens it already generated, then continues from its pending token."""
+        self.eng.release(j.req)
+        j.req = None
+        (self.running if j in self.running else self.prefilling).remove(j)
+        self.waiting.appendleft(j)
+        self.preemptions += 1
+
     def _step(self) -> None:
+        eng = self.eng
         budget = self.prefill_tokens
+        reserve = len(self.running)                 # headroom: one new page per running decode
+        committed = 0
         batch: List[Job] = []
         counts: List[int] = []
-        # continue chunked prefills first, then admit new requests while the token budget and batch size allow
+        # continue chunked prefills first, then admit new requests while the token budget, the batch size and the
+        # free KV pages allow
         for j in list(self.prefilling):
             if budget <= 0:
                 break
             n = min(budget, j.req.seq_len - j.req.n_cached)
+            need = eng.pages_for(j.req, j.req.n_cached + n)
+            if need > eng.pages_available() - reserve - committed:
+                break
+            committed += need
             batch.append(j)
             counts.append(n)
             budget -= n
         while self.waiting and budget > 0 and len(self.running) + len(self.prefilling) + 1 <= self.max_running:
-            j = self.waiting.popleft()
-            j.req = self.eng.add_request(j.prompt)
+            j = self.waiting[0]
+            req = eng.add_request(j.tokens())
+            n = min(budget, req.seq_len - req.n_cached)     # a cached prefix (prefix reuse) is skipped
+            need = eng.pages_for(req, req.n_cached + n)
+            if need > eng.pages_available() - reserve - committed:
+                eng.release(req)                            # give back the shared prefix pages
+                break
+            self.waiting.popleft()
+            j.req, j.admit = req, self._admits
+            self._admits += 1
+            committed += need
             self.prefilling.append(j)
-            n = min(budget, j.req.seq_len - j.req.n_cached)     # a cached prefix (prefix reuse) is skipped
             batch.append(j)
             counts.append(n)
             budget -= n
         if batch:
             self.steps["prefill"] += 1
-            whole = all(j.req.n_cached == 0 and n == len(j.prompt) for j, n in zip(batch, counts))
+            whole = all(j.req.n_cached == 0 and n == j.req.seq_len for j, n in zip(batch, counts))
             if whole:
-                logits = self.eng.prefill([j.req for j in batch])
+                logits = eng.prefill([j.req for j in batch])
             else:
-                if self.eng.cfg.late_layer_start >= 0:
+                if eng.cfg.late_layer_start >= 0:
                     for j in batch:
                         if j.req.n_cached == 0:
-                            j.req.late_from = max(0, len(j.prompt) - self.eng.cfg.late_replay)
-                logits = self.eng._prefill_rows([j.req for j in batch], counts)
+                            j.req.late_from = max(0, j.req.seq_len - eng.cfg.late_replay)
+                logits = eng._prefill_rows([j.req for j in batch], counts)
             for j, row in zip(batch, logits):
-                if j.req.n_cached == j.req.seq_len:             # prompt complete: first output token
+                if j.req.n_cached == j.req.seq_len:             # prompt complete
                     self.prefilling.remove(j)
-                    self._take(j, j.sample(row))
+                    if j.out:                                   # resumed after a preemption: already sampled
+                        j.pending = j.out[-1]
+                        self.running.append(j)
+                    else:
+                        self._take(j, j.sample(row))
             return
         if not self.running:
+            if self.prefilling:                     # chunked prefills that cannot all fit: retract the youngest
+                if len(self.prefilling) > 1:
+                    self._retract(max(self.prefilling, key=lambda j: j.admit))
+                    return
+            if self.waiting or self.prefilling:
+                raise RuntimeError("KV cache too small for the next request")
             return
+        # decode every running job; if the pages for this step are short, preempt the youngest jobs first
+        while True:
+            need = sum(eng.pages_for(j.req, j.req.seq_len + 1) for j in self.running)
+            if need <= eng.pages_available():
+                break
+            oldest = min(self.running, key=lambda j: j.admit)      # always keeps making progress
+            victims = sorted((j for j in self.running + self.prefilling if j is not oldest), key=lambda j: -j.admit)
+            if not victims:
+                raise RuntimeError("KV cache too small for the running request")
+            self._retract(victims[0])
         self.steps["decode"] += 1
         run, self.running = self.running, []
-        logits = self.eng.decode([j.req for j in run], [j.pending for j in run])
+        logits = eng.decode([j.req for j in run], [j.pending for j in run])
         for j, row in zip(run, logits):
             self._take(j, j.sample(row))
 

@@ -97,3 +97,31 @@ def test_scheduler_spmd_two_ranks():
         assert p.exitcode == 0
     for rank, outs in res:
         assert outs == want, rank
+
+
+def test_preemption_under_kv_pressure_keeps_outputs():
+    """A cache far smaller than the batch's final footprint: admission waits for pages, decode preempts the youngest
+    requests (their KV is freed and recomputed on readmission), and every request still gets the tokens it gets
+    with a large cache."""
+    cfg = tiny_config()
+    w = init_weights(cfg, seed=0)
+    prompts = [((torch.arange(30) * (k + 3) + k) % cfg.vocab_size).tolist() for k in range(4)]
+
+    def serve(num_pages, prefill_tokens=4096):
+        eng = Engine(cfg, "cpu", source=WeightSource(cfg, state=w), num_pages=num_pages, page_size=16)
+        s = Scheduler(eng, prefill_tokens=prefill_tokens)
+        ids = [s.submit(p, 40) for p in prompts]
+        out = s.run()
+        assert eng.cache.alloc.num_free() == num_pages - 1                 # every page back (scratch page kept)
+        return [out[i] for i in ids], s
+
+    ref, s_big = serve(64)
+    assert s_big.preemptions == 0
+    got, s_small = serve(10)                       # 9 usable pages; the four requests end at 5 pages each
+    assert s_small.preemptions > 0
+    assert got == ref
+    got2, s_chunk = serve(10, prefill_tokens=20)   # chunked prefills competing for pages
+    assert got2 == ref
+    eng = Engine(cfg, "cpu", source=WeightSource(cfg, state=w), num_pages=4, page_size=16)
+    with pytest.raises(ValueError):
+        Scheduler(eng).submit(list(range(40)), 20)                          # 60 tokens > 3 pages x 16
