@@ -71,6 +71,7 @@ class Scheduler:
         self.prefilling: List[Job] = []        # admitted, prompt partly cached (chunked prefill)
         self.running: List[Job] = []
         self.finished: Dict[int, Job] = {}
+        self.jobs: Dict[int, Job] = {}         # submitted, not yet finished (a job's ``out`` grows token by token)
         self._next = 0
         self._admits = 0
         self.preemptions = 0
@@ -85,6 +86,7 @@ class Scheduler:
         j = Job(self._next, list(prompt), max_new_tokens, tuple(stop), temperature, top_k, seed)
         self._next += 1
         self.waiting.append(j)
+        self.jobs[j.jid] = j
         return j.jid
 
     def idle(self) -> bool:
@@ -94,6 +96,7 @@ class Scheduler:
         j.done = True
         self.eng.release(j.req)
         self.finished[j.jid] = j
+        self.jobs.pop(j.jid, None)
 
     def _take(self, j: Job, tok: int):
         """Record a sampled token; retire the job when it is complete."""

@@ -3,7 +3,9 @@
 Endpoints:
 
 * ``POST /generate`` with ``{"input_ids": [...], "max_new_tokens": n, "stop": [...], "temperature": t,
-  "top_k": k, "seed": s}`` returns ``{"output_ids": [...]}`` once the request finished;
+  "top_k": k, "seed": s}`` returns ``{"output_ids": [...]}`` once the request finished; with ``"stream": true``
+  the reply is a server-sent event stream: one ``data: {"token": t}`` event per generated token as the scheduler
+  produces it, then ``data: {"output_ids": [...]}`` and ``data: [DONE]``;
 * ``GET /metrics``: Prometheus text exposition of the engine's step metrics (tokens/s, TPOT percentiles);
 * ``GET /health``.
 
@@ -13,7 +15,9 @@ out (tokenisation belongs to the client).  Run with ``python -m carbon_b200.engi
 GPU) or build ``make_app(engine)`` around an engine of your own.
 """
 import argparse
+import json
 import threading
+from contextlib import asynccontextmanager
 from typing import List
 
 from .engine import Engine
@@ -22,7 +26,7 @@ from .scheduler import Scheduler
 
 def make_app(engine: Engine, max_running: int = 256, prefill_tokens: int = 32768):
     from fastapi import FastAPI, HTTPException
-    from fastapi.responses import PlainTextResponse
+    from fastapi.responses import PlainTextResponse, StreamingResponse
     from pydantic import BaseModel, Field
 
     class GenerateRequest(BaseModel):
@@ -32,6 +36,7 @@ def make_app(engine: Engine, max_running: int = 256, prefill_tokens: int = 32768
         temperature: float = 0.0
         top_k: int = 0
         seed: int = 0
+        stream: bool = False
 
     sched = Scheduler(engine, max_running=max_running, prefill_tokens=prefill_tokens)
     lock = threading.Condition()
@@ -57,17 +62,16 @@ def make_app(engine: Engine, max_running: int = 256, prefill_tokens: int = 32768
                 lock.notify_all()
 
     worker = threading.Thread(target=loop, name="carbon-scheduler", daemon=True)
-    app = FastAPI(title="carbon-b200")
 
-    @app.on_event("startup")
-    def _start():
+    @asynccontextmanager
+    async def lifespan(_app):
         worker.start()
-
-    @app.on_event("shutdown")
-    def _stop():
+        yield
         with lock:
             stop_flag["stop"] = True
             lock.notify_all()
+
+    app = FastAPI(title="carbon-b200", lifespan=lifespan)
 
     @app.get("/health")
     def health():
@@ -80,15 +84,46 @@ def make_app(engine: Engine, max_running: int = 256, prefill_tokens: int = 32768
         with lock:
             if stop_flag["error"]:
                 raise HTTPException(status_code=500, detail="engine failed: " + stop_flag["error"])
-            jid = sched.submit(req.input_ids, req.max_new_tokens, tuple(req.stop), req.temperature, req.top_k,
-                               req.seed)
+            try:
+                jid = sched.submit(req.input_ids, req.max_new_tokens, tuple(req.stop), req.temperature, req.top_k,
+                                   req.seed)
+            except ValueError as e:                 # longer than the KV cache can ever hold
+                raise HTTPException(status_code=400, detail=str(e))
+            job = sched.jobs[jid]
             lock.notify_all()
+            if req.stream:
+                return StreamingResponse(_events(jid, job), media_type="text/event-stream")
             while jid not in done:
                 if stop_flag["error"]:
                     raise HTTPException(status_code=500, detail="engine failed: " + stop_flag["error"])
                 lock.wait(timeout=1.0)
             out = done.pop(jid)
         return {"output_ids": out}
+
+    def _events(jid, job):
+        sent = 0
+        while True:
+            with lock:
+                while len(job.out) == sent and not job.done and not stop_flag["error"]:
+                    lock.wait(timeout=1.0)
+                if stop_flag["error"] and not job.done:
+                    err = stop_flag["error"]
+                    new, finished = [], None
+                else:
+                    err = None
+                    new, finished = job.out[sent:], job.done
+                    if finished:
+                        done.pop(jid, None)
+            if err is not None:
+                yield "data: " + json.dumps({"error": "engine failed: " + err}) + "\n\n"
+                return
+            for t in new:
+                yield "data: " + json.dumps({"token": t}) + "\n\n"
+            sent += len(new)
+            if finished:
+                yield "data: " + json.dumps({"output_ids": list(job.out)}) + "\n\n"
+                yield "data: [DONE]\n\n"
+                return
 
     @app.get("/metrics", response_class=PlainTextResponse)
     def metrics():
