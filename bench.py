@@ -46,6 +46,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=0, help="override layer count (0 = config's)")
     ap.add_argument("--mem-frac", type=float, default=0.62, help="HBM fraction for weights (rest: cache, acts)")
     ap.add_argument("--profile", action="store_true", help="print per-region device times (stderr)")
+    ap.add_argument("--trace-dir", default=None,
+                    help="with --profile: write Chrome trace files of the traced decode and prefill steps here "
+                         "(one per rank)")
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                     help="multi-GPU data movement: our NVLink kernels (fused) or the NCCL baseline")
     ap.add_argument("--attn", default="tp", choices=["tp", "dp"],
@@ -291,6 +294,9 @@ def main():
             eng.decode(reqs, next_ids())
         eng.cuda_graphs = graphs
         tables.append("== decode regions (eager) ==\n" + t.table())
+        if args.trace_dir:
+            os.makedirs(args.trace_dir, exist_ok=True)
+            t.chrome_trace(os.path.join(args.trace_dir, f"decode_rank{rank}.json"), pid=rank)
     for r in reqs:
         eng.release(r)
     launches = count_launches(eng, P, S)
@@ -298,6 +304,8 @@ def main():
         with tracing() as t:
             prefill_step()
         tables.append("== prefill regions ==\n" + t.table())
+        if args.trace_dir:
+            t.chrome_trace(os.path.join(args.trace_dir, f"prefill_rank{rank}.json"), pid=rank)
         if rank == 0:
             print("\n".join(tables), file=sys.stderr, flush=True)
     if world > 1:

@@ -9,10 +9,18 @@ inside the step:
     with tracing() as t:
         engine.prefill(reqs)
     print(t.table())
+    t.chrome_trace("prefill.json")      # open in Perfetto / chrome://tracing: one track per stream
+
+Without a GPU (the CPU engine) the regions are timed with the host clock instead, so the same tables and traces
+come out of CPU runs.  Regions inside CUDA-graph capture are skipped (graph replays show up as one region of the
+caller).
 """
 from __future__ import annotations
 
 import contextlib
+import json
+import os
+import time
 from collections import defaultdict
 from typing import Dict, List, Optional, Tuple
 
@@ -23,15 +31,36 @@ _ACTIVE: Optional["Tracer"] = None
 
 class Tracer:
     def __init__(self):
-        self.events: List[Tuple[str, torch.cuda.Event, torch.cuda.Event]] = []
+        # (name, start, end, stream id): CUDA events on the GPU, host perf_counter seconds on the CPU
+        self.events: List[Tuple[str, object, object, int]] = []
+
+    def _spans(self) -> List[Tuple[str, float, float, int]]:
+        """(name, start ms, duration ms, stream) of every region, starts relative to the first region."""
+        if not self.events:
+            return []
+        first = self.events[0][1]
+        if isinstance(first, float):
+            return [(n, (a - first) * 1e3, (b - a) * 1e3, st) for n, a, b, st in self.events]
+        torch.cuda.synchronize()
+        return [(n, first.elapsed_time(a), a.elapsed_time(b), st) for n, a, b, st in self.events]
 
     def totals(self) -> Dict[str, Tuple[int, float]]:
-        torch.cuda.synchronize()
         agg: Dict[str, List[float]] = defaultdict(lambda: [0, 0.0])
-        for name, a, b in self.events:
+        for name, _, dur, _ in self._spans():
             agg[name][0] += 1
-            agg[name][1] += a.elapsed_time(b)
+            agg[name][1] += dur
         return {k: (int(v[0]), float(v[1])) for k, v in agg.items()}
+
+    def chrome_trace(self, path: str, pid: Optional[int] = None) -> int:
+        """Write the regions as a Chrome trace-event file (complete events, microseconds; one thread per stream,
+        the process id defaults to this rank).  Returns the number of events written."""
+        if pid is None:
+            pid = int(os.environ.get("RANK", "0"))
+        ev = [{"name": n, "ph": "X", "ts": round(t0 * 1e3, 3), "dur": round(d * 1e3, 3), "pid": pid, "tid": st,
+               "cat": n.split(".")[0]} for n, t0, d, st in self._spans()]
+        with open(path, "w") as f:
+            json.dump({"traceEvents": ev, "displayTimeUnit": "ms"}, f)
+        return len(ev)
 
     def table(self, top: int = 40) -> str:
         tot = self.totals()
@@ -55,15 +84,26 @@ def tracing():
 @contextlib.contextmanager
 def region(name: str):
     t = _ACTIVE
-    if t is None or not torch.cuda.is_available() or torch.cuda.is_current_stream_capturing():
+    if t is None:
+        yield
+        return
+    if not torch.cuda.is_available():
+        a = time.perf_counter()
+        try:
+            yield
+        finally:
+            t.events.append((name, a, time.perf_counter(), 0))
+        return
+    if torch.cuda.is_current_stream_capturing():
         yield
         return
     torch.cuda.nvtx.range_push(name)
+    stream = torch.cuda.current_stream()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
+    a.record(stream)
     try:
         yield
     finally:
-        b.record()
+        b.record(stream)
         torch.cuda.nvtx.range_pop()
-        t.events.append((name, a, b))
+        t.events.append((name, a, b, int(stream.stream_id)))

@@ -43,3 +43,24 @@ def test_bench_roofline_estimate():
     assert 0 < r1["prefill_frac"] < 1 and 0 < r1["decode_frac"] < 1
     r8 = b.roofline(cfg, 8, 4, 4096, 32, 4096, 1680.0, 74.0, peak)
     assert r8["decode_gb_per_gpu_step"] < r1["decode_gb_per_gpu_step"] / 4          # 32 experts per rank
+
+
+def test_tracing_on_cpu_and_chrome_trace(tmp_path):
+    import json
+
+    from carbon_b200.config import tiny_config
+    from carbon_b200.engine.engine import Engine
+    from carbon_b200.utils.trace import tracing
+
+    eng = Engine(tiny_config(), "cpu", num_pages=16, page_size=16)
+    with tracing() as t:
+        eng.generate([list(range(20)), list(range(5, 17))], 3)
+    tot = t.totals()
+    assert any(k.startswith("attn.") for k in tot) and any(k.startswith("moe.") for k in tot)
+    assert all(c > 0 and ms >= 0 for c, ms in tot.values())
+    assert "region" in t.table()
+    path = tmp_path / "trace.json"
+    n = t.chrome_trace(str(path))
+    ev = json.loads(path.read_text())["traceEvents"]
+    assert n == len(ev) == len(t.events) > 0
+    assert all(e["ph"] == "X" and e["dur"] >= 0 and e["ts"] >= 0 for e in ev)
