@@ -38,6 +38,60 @@ def is_fp8_name(name: str) -> bool:
     return name.endswith(FP8_SUFFIXES)
 
 
+# Hugging Face DeepSeek-V3 / V3.2 module names -> this loader's names (the same correspondence DeepSeek's own
+# inference code applies when it converts those checkpoints).  Linear layers whose name here has no ".weight" (the
+# FFN matrices) take "<name>_scale_inv" for the HF "weight_scale_inv".
+_HF_ATTN = {"q_a_proj": "attn.wq_a", "q_b_proj": "attn.wq_b", "q_proj": "attn.wq", "kv_a_proj_with_mqa": "attn.wkv_a",
+            "kv_b_proj": "attn.wkv_b", "o_proj": "attn.wo", "q_a_layernorm": "attn.q_norm",
+            "kv_a_layernorm": "attn.kv_norm", "indexer.wq_b": "attn.indexer.wq", "indexer.wk": "attn.indexer.wk",
+            "indexer.k_norm": "attn.indexer.k_norm", "indexer.weights_proj": "attn.indexer.weights_proj"}
+_HF_FFN = {"gate_proj": "w1", "down_proj": "w2", "up_proj": "w3"}
+_HF_LAYER_RE = re.compile(r"^model\.layers\.(\d+)\.(.+)$")
+
+
+def hf_to_internal(name: str, n_layers: int) -> Optional[str]:
+    """Internal name of a Hugging Face DeepSeek checkpoint tensor; None for tensors the model does not use (layers
+    at or beyond ``n_layers``, e.g. the multi-token-prediction layer).  Names not in HF form pass through."""
+    top = {"model.embed_tokens.weight": "embed.weight", "model.norm.weight": "norm.weight",
+           "lm_head.weight": "head.weight"}
+    if name in top:
+        return top[name]
+    m = _HF_LAYER_RE.match(name)
+    if m is None:
+        return None if name.startswith("model.") else name
+    layer, rest = int(m.group(1)), m.group(2)
+    if layer >= n_layers:
+        return None
+    pre = f"layers.{layer}."
+    if rest == "input_layernorm.weight":
+        return pre + "attn_norm.weight"
+    if rest == "post_attention_layernorm.weight":
+        return pre + "ffn_norm.weight"
+    if rest.startswith("self_attn."):
+        mod, _, leaf = rest[len("self_attn."):].rpartition(".")
+        if mod in _HF_ATTN and leaf in ("weight", "bias", "weight_scale_inv"):
+            return pre + _HF_ATTN[mod] + "." + leaf
+        return None
+    if rest.startswith("mlp."):
+        r = rest[len("mlp."):]
+        if r == "gate.weight":
+            return pre + "ffn.gate.weight"
+        if r == "gate.e_score_correction_bias":
+            return pre + "ffn.gate.bias"
+        mod, _, leaf = r.rpartition(".")
+        if leaf not in ("weight", "weight_scale_inv"):
+            return None
+        suffix = "" if leaf == "weight" else "_scale_inv"
+        parts = mod.split(".")
+        if len(parts) == 3 and parts[0] == "experts" and parts[2] in _HF_FFN:
+            return f"{pre}ffn.experts.{int(parts[1])}.{_HF_FFN[parts[2]]}{suffix}"
+        if len(parts) == 2 and parts[0] == "shared_experts" and parts[1] in _HF_FFN:
+            return f"{pre}ffn.shared.{_HF_FFN[parts[1]]}{suffix}"
+        if len(parts) == 1 and parts[0] in _HF_FFN:
+            return f"{pre}ffn.{_HF_FFN[parts[0]]}{suffix}"
+    return None
+
+
 def save_checkpoint(state: Dict[str, torch.Tensor], path: str, shard_bytes: int = 2 << 30,
                     per_expert: bool = False, mxfp4_experts: bool = False) -> None:
     """Write ``state`` (fp32 tensors) as fp8 block-scaled safetensors shards + an index JSON (routed experts in MXFP4
@@ -98,7 +152,10 @@ def save_checkpoint(state: Dict[str, torch.Tensor], path: str, shard_bytes: int 
 
 
 class CheckpointSource(WeightSource):
-    """WeightSource over a directory of safetensors shards (block-scaled fp8 names dequantised on load)."""
+    """WeightSource over a directory of safetensors shards (block-scaled fp8 names dequantised on load).  Both this
+    loader's names and Hugging Face DeepSeek names (``model.layers.N.self_attn.q_a_proj.weight``, ``weight_scale_inv``,
+    ``mlp.experts.E.gate_proj`` ...) are accepted; parameters that HF DeepSeek checkpoints do not carry (mHC) must then
+    come under this loader's names in the same directory."""
 
     def __init__(self, cfg: ModelConfig, path: str, layer_sets: Optional[int] = None):
         super().__init__(cfg, state=None, seed=0, layer_sets=layer_sets)
@@ -116,6 +173,16 @@ class CheckpointSource(WeightSource):
                     with safe_open(os.path.join(path, fn), "pt") as h:
                         for n in h.keys():
                             wm[n] = fn
+        self.stored: Dict[str, str] = {}                 # internal name -> name in the file (HF checkpoints)
+        if any(n.startswith("model.") for n in wm):
+            conv = {}
+            for n, fn in wm.items():
+                k = hf_to_internal(n, cfg.n_layers)
+                if k is not None:
+                    conv[k] = fn
+                    if k != n:
+                        self.stored[k] = n
+            wm = conv
         self.weight_map = wm
         self._handles = {}
         self._safe_open = safe_open
@@ -126,7 +193,7 @@ class CheckpointSource(WeightSource):
         if h is None:
             h = self._safe_open(os.path.join(self.path, fn), "pt")
             self._handles[fn] = h
-        return h.get_tensor(name)
+        return h.get_tensor(self.stored.get(name, name))
 
     def has(self, name: str) -> bool:
         return name in self.weight_map

@@ -1,5 +1,7 @@
 """fp8 block-scaled safetensors checkpoints: save -> load round trip; the engine served from a checkpoint equals
 the engine served from the same (fp8-rounded) weights in memory."""
+import os
+
 import torch
 
 from carbon_b200.config import tiny_config
@@ -65,3 +67,58 @@ def test_mxfp4_experts_checkpoint(tmp_path):
     e1 = Engine(cfg, "cpu", source=CheckpointSource(cfg, str(tmp_path / "mx0")), num_pages=8, page_size=16)
     e2 = Engine(cfg, "cpu", source=WeightSource(cfg, state=st), num_pages=8, page_size=16)
     assert e1.generate(prompts, 4) == e2.generate(prompts, 4)
+
+
+def _to_hf(name):
+    """This test's own spelling of Hugging Face DeepSeek names (written out independently of the loader's table)."""
+    import re
+
+    top = {"embed.weight": "model.embed_tokens.weight", "norm.weight": "model.norm.weight",
+           "head.weight": "lm_head.weight"}
+    if name in top:
+        return top[name]
+    m = re.match(r"^layers\.(\d+)\.(.+)$", name)
+    if m is None:
+        return name
+    i, rest = m.group(1), m.group(2)
+    sub = [("attn_norm.weight", "input_layernorm.weight"), ("ffn_norm.weight", "post_attention_layernorm.weight"),
+           ("attn.wq_a.", "self_attn.q_a_proj."), ("attn.wq_b.", "self_attn.q_b_proj."),
+           ("attn.wkv_a.", "self_attn.kv_a_proj_with_mqa."), ("attn.wkv_b.", "self_attn.kv_b_proj."),
+           ("attn.wo.", "self_attn.o_proj."), ("attn.q_norm.", "self_attn.q_a_layernorm."),
+           ("attn.kv_norm.", "self_attn.kv_a_layernorm."), ("attn.indexer.wq.", "self_attn.indexer.wq_b."),
+           ("attn.indexer.", "self_attn.indexer."), ("ffn.gate.weight", "mlp.gate.weight"),
+           ("ffn.gate.bias", "mlp.gate.e_score_correction_bias")]
+    for a, b in sub:
+        if rest.startswith(a):
+            return f"model.layers.{i}.{b}{rest[len(a):]}"
+    m = re.match(r"^ffn\.(experts\.\d+\.|shared\.|)(w[123])(_scale_inv)?$", rest)
+    if m:
+        grp = {"": "", "shared.": "shared_experts."}.get(m.group(1), m.group(1))
+        proj = {"w1": "gate_proj", "w2": "down_proj", "w3": "up_proj"}[m.group(2)]
+        return f"model.layers.{i}.mlp.{grp}{proj}.weight{m.group(3) or ''}"
+    return name                                           # mHC parameters keep this loader's names
+
+
+def test_hugging_face_names_load(tmp_path):
+    from safetensors.torch import load_file, save_file
+
+    cfg = tiny_config()
+    w = init_weights(cfg, seed=0)
+    d = tmp_path / "ours"
+    save_checkpoint(w, str(d), per_expert=True)
+    tensors = {}
+    for fn in sorted(os.listdir(d)):
+        if fn.endswith(".safetensors"):
+            tensors.update(load_file(str(d / fn)))
+    hf = {_to_hf(k): v for k, v in tensors.items()}
+    assert any(k.startswith("model.layers.0.mlp.experts.1.up_proj.weight_scale_inv") for k in hf)
+    hf[f"model.layers.{cfg.n_layers}.eh_proj.weight"] = torch.zeros(4, 4)   # an MTP layer: ignored
+    h = tmp_path / "hf"
+    h.mkdir()
+    save_file(hf, str(h / "model.safetensors"))
+    a, b = CheckpointSource(cfg, str(d)), CheckpointSource(cfg, str(h))
+    for k in w:
+        assert torch.equal(a.get(k, "cpu"), b.get(k, "cpu")), k
+    ref = Engine(cfg, "cpu", source=a, num_pages=16, page_size=16).generate([list(range(20))], 4)
+    got = Engine(cfg, "cpu", source=b, num_pages=16, page_size=16).generate([list(range(20))], 4)
+    assert got == ref
