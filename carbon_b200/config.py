@@ -100,7 +100,7 @@ class ModelConfig:
     norm_topk_prob: bool = True
     swiglu_limit: float = 0.0          # 0 => no clamp
     # mHC (manifold-constrained hyper-connections)
-    hc_mult: int = 4
+    hc_mult: int = 4   # 0: no hyper-connections (one residual stream, x + f(norm(x)): DeepSeek-V3 / V3.2)
     sinkhorn_iters: int = 20
     hc_eps: float = 1e-6
     rms_eps: float = 1e-6
@@ -126,6 +126,16 @@ class ModelConfig:
     def head_out_dim(self) -> int:
         """Per-head attention output width (the input of the output projection per head)."""
         return self.kv_lora_rank if self.attn_kind == "latent_mqa" else self.v_head_dim
+
+    @property
+    def plain_residual(self) -> bool:
+        """hc_mult == 0: the standard pre-norm residual instead of mHC (checkpoints without hyper-connections)."""
+        return self.hc_mult == 0
+
+    @property
+    def hc_streams(self) -> int:
+        """Residual streams carried between sublayers (one for the plain residual)."""
+        return max(1, self.hc_mult)
 
     @property
     def hc_mix_dim(self) -> int:

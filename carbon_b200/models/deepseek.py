@@ -148,6 +148,9 @@ class DeepseekModel:
         self.cfg = cfg
         self.device = torch.device(device)
         self.on_gpu = self.device.type == "cuda"
+        if cfg.plain_residual and cfg.engram_layers and self.on_gpu:
+            raise NotImplementedError("Engram on the GPU gates the mHC streams; plain-residual models (hc_mult=0) "
+                                      "with Engram layers run on the CPU engine only")
         self.pctx = pctx if pctx is not None else ParallelCtx.single()
         self.fp8 = fp8
         self.trace = None          # set to a list to record (name, tensor) at sublayer boundaries (debugging)
@@ -171,7 +174,8 @@ class DeepseekModel:
         self.v_hi = min(V, self.v_lo + vs)
         self.embed = get("embed.weight", slice(self.v_lo, self.v_hi)).to(self.act_dtype).contiguous()
         self.head_w = Lin(get("head.weight", slice(self.v_lo, self.v_hi)), dev, fp8=False)
-        self.head_hc = make_hc(get("head_hc.fn"), get("head_hc.base"), get("head_hc.scale"), dev)
+        self.head_hc = None if cfg.plain_residual else \
+            make_hc(get("head_hc.fn"), get("head_hc.base"), get("head_hc.scale"), dev)
         self.norm_w = get("norm.weight")
         # layers whose weights are tied (WeightSource.layer_sets) share one Layer object
         built: Dict[str, Layer] = {}
@@ -265,8 +269,11 @@ class DeepseekModel:
         cfg, dev, pc = self.cfg, self.device, self.pctx
         L = Layer()
         p = f"layers.{i}."
-        L.attn_hc = make_hc(get(p + "attn_hc.fn"), get(p + "attn_hc.base"), get(p + "attn_hc.scale"), dev)
-        L.ffn_hc = make_hc(get(p + "ffn_hc.fn"), get(p + "ffn_hc.base"), get(p + "ffn_hc.scale"), dev)
+        if cfg.plain_residual:
+            L.attn_hc = L.ffn_hc = None
+        else:
+            L.attn_hc = make_hc(get(p + "attn_hc.fn"), get(p + "attn_hc.base"), get(p + "attn_hc.scale"), dev)
+            L.ffn_hc = make_hc(get(p + "ffn_hc.fn"), get(p + "ffn_hc.base"), get(p + "ffn_hc.scale"), dev)
         L.attn_norm = get(p + "attn_norm.weight")
         L.ffn_norm = get(p + "ffn_norm.weight")
         H, Hl, dn, dr, dv, r = cfg.n_heads, self.H_local, cfg.qk_nope_head_dim, cfg.qk_rope_head_dim, \
@@ -380,6 +387,19 @@ class DeepseekModel:
             sf = empty_sf(T, D, X.device)
         ext().mhc_pre_norm(X, pre, w, self.cfg.rms_eps, y, q, sf, None)
         return y, ((q, sf) if want_fp8 else None)
+
+    def plain_norm(self, X, w, want_fp8: bool):
+        """Plain pre-norm residual: RMSNorm(x)·w of the single stream -> (h, (fp8 q, sf) or None)."""
+        x = X[:, 0]
+        if not self.on_gpu:
+            return R.rms_norm(x, w, self.cfg.rms_eps), None
+        if want_fp8:
+            return C.rms_norm(x, w, self.cfg.rms_eps, want_bf16=True, want_fp8=True)
+        return C.rms_norm(x, w, self.cfg.rms_eps), None
+
+    def plain_add(self, X, out):
+        """x + f(x): the sublayer output joins the single residual stream."""
+        return X + out.to(X.dtype).view(X.shape[0], 1, X.shape[2])
 
     def post_mix(self, X, out, post, comb):
         if not self.on_gpu:
@@ -731,7 +751,7 @@ class DeepseekModel:
         cfg = self.cfg
         if not self.on_gpu and self.pctx.world == 1:
             T = ids.shape[0]
-            X = self.embed[ids.long()][:, None, :].expand(T, cfg.hc_mult, cfg.hidden_size).clone()
+            X = self.embed[ids.long()][:, None, :].expand(T, cfg.hc_streams, cfg.hidden_size).clone()
             return X, None
         return self.pctx.embed(self, ids)
 
@@ -754,6 +774,15 @@ class DeepseekModel:
             if L.engram is not None:
                 with region("engram"):
                     X, sumsq = self.engram(i, X, sumsq, fb, cache)
+            if cfg.plain_residual:
+                with region("norm"):
+                    h, hq = self.plain_norm(X, L.attn_norm, want_fp8=self.on_gpu)
+                a = self.attention(i, h, hq, fb, cache)
+                X = self.plain_add(X, a)
+                with region("norm"):
+                    h, hq = self.plain_norm(X, L.ffn_norm, want_fp8=self.on_gpu)
+                X = self.plain_add(X, self.ffn(i, h, hq))
+                continue
             with region("mhc.coeffs"):
                 pre, post, comb = self.hc_coeffs(X, sumsq, L.attn_hc)
             with region("mhc.pre_norm"):
@@ -822,7 +851,9 @@ class DeepseekModel:
                 local_rows = rows.long()
             X = X[local_rows].contiguous()
             sumsq = sumsq[local_rows] if sumsq is not None else None
-        if not self.on_gpu:
+        if cfg.plain_residual:
+            y, _ = self.plain_norm(X, self.norm_w, want_fp8=False)
+        elif not self.on_gpu:
             pre = R.mhc_head_coeffs(X, self.head_hc.fn, self.head_hc.base, self.head_hc.scale, cfg.hc_eps,
                                     cfg.rms_eps)
             y = R.rms_norm(R.mhc_pre_mix(X, pre), self.norm_w, cfg.rms_eps)

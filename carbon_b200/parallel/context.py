@@ -66,7 +66,7 @@ class ParallelCtx:
 
         cfg = model.cfg
         T = ids.shape[0]
-        X = torch.empty(T, cfg.hc_mult, cfg.hidden_size, dtype=torch.bfloat16, device=ids.device)
+        X = torch.empty(T, cfg.hc_streams, cfg.hidden_size, dtype=torch.bfloat16, device=ids.device)
         sumsq = torch.empty(T, device=ids.device)
         ext().embed_hc(model.embed, model.v_lo, ids.to(torch.int32).contiguous(), X, sumsq)
         return X, sumsq

@@ -161,7 +161,7 @@ class DistCtx(ParallelCtx):
             sel = torch.nonzero(own == s, as_tuple=True)[0]
             rows[sel] = recv[off: off + sel.numel()]
             off += sel.numel()
-        X = rows[:, None, :].expand(hi - lo, cfg.hc_mult, cfg.hidden_size).contiguous()
+        X = rows[:, None, :].expand(hi - lo, cfg.hc_streams, cfg.hidden_size).contiguous()
         sumsq = X.float().pow(2).sum((1, 2)) if model.on_gpu else None
         return X, sumsq
 

@@ -174,7 +174,7 @@ class FusedCtx(DistCtx):
         cfg = model.cfg
         lo, hi = self.local
         ids = ids_all[lo:hi].to(torch.int32).contiguous()
-        X = torch.empty(hi - lo, cfg.hc_mult, cfg.hidden_size, dtype=torch.bfloat16, device=ids.device)
+        X = torch.empty(hi - lo, cfg.hc_streams, cfg.hidden_size, dtype=torch.bfloat16, device=ids.device)
         sumsq = torch.empty(hi - lo, device=ids.device)
         b, per = self._embed
         ext().embed_peer(b.peers, per, ids, X, sumsq)

@@ -29,12 +29,12 @@ from . import ops
 # ----------------------------------------------------------------------------------------------------------------------
 def param_shapes(cfg: ModelConfig) -> "OrderedDict[str, Tuple[Tuple[int, ...], str]]":
     """name -> (shape, init) with init in {"normal", "ones", "zeros"}."""
-    D, H, hc = cfg.hidden_size, cfg.n_heads, cfg.hc_mult
+    D, H, hc = cfg.hidden_size, cfg.n_heads, cfg.hc_streams
     p: "OrderedDict[str, Tuple[Tuple[int, ...], str]]" = OrderedDict()
     p["embed.weight"] = ((cfg.vocab_size, D), "normal")
     for i in range(cfg.n_layers):
         L = f"layers.{i}."
-        for sub in ("attn_hc", "ffn_hc"):
+        for sub in (() if cfg.plain_residual else ("attn_hc", "ffn_hc")):
             p[L + sub + ".fn"] = ((cfg.hc_mix_dim, hc * D), "normal")
             p[L + sub + ".base"] = ((cfg.hc_mix_dim,), "normal")
             p[L + sub + ".scale"] = ((3,), "ones")
@@ -89,9 +89,10 @@ def param_shapes(cfg: ModelConfig) -> "OrderedDict[str, Tuple[Tuple[int, ...], s
             p[L + "ffn.w1"] = ((I, D), "normal")
             p[L + "ffn.w3"] = ((I, D), "normal")
             p[L + "ffn.w2"] = ((D, I), "normal")
-    p["head_hc.fn"] = ((hc, hc * D), "normal")
-    p["head_hc.base"] = ((hc,), "normal")
-    p["head_hc.scale"] = ((1,), "ones")
+    if not cfg.plain_residual:
+        p["head_hc.fn"] = ((hc, hc * D), "normal")
+        p["head_hc.base"] = ((hc,), "normal")
+        p["head_hc.scale"] = ((1,), "ones")
     p["norm.weight"] = ((D,), "ones")
     p["head.weight"] = ((cfg.vocab_size, D), "normal")
     return p
@@ -252,6 +253,8 @@ class RefModel:
 
     def hc_sublayer(self, X, prefix: str, norm_w: torch.Tensor, fn_apply) -> torch.Tensor:
         cfg, w = self.cfg, self.w
+        if cfg.plain_residual:                  # x + f(RMSNorm(x)·w)
+            return X + fn_apply(ops.rms_norm(X[:, 0], norm_w, cfg.rms_eps))[:, None]
         pre, post, comb = ops.mhc_coeffs(X, w[prefix + ".fn"], w[prefix + ".base"], w[prefix + ".scale"],
                                          cfg.hc_mult, cfg.sinkhorn_iters, cfg.hc_eps, cfg.rms_eps)
         y = ops.rms_norm(ops.mhc_pre_mix(X, pre), norm_w, cfg.rms_eps)
@@ -266,7 +269,7 @@ class RefModel:
         pos = torch.arange(T) if pos is None else pos
         self._dsa = {}
         self._ids = ids
-        X = w["embed.weight"][ids.long()][:, None, :].expand(T, cfg.hc_mult, cfg.hidden_size).clone()
+        X = w["embed.weight"][ids.long()][:, None, :].expand(T, cfg.hc_streams, cfg.hidden_size).clone()
         for i in range(cfg.n_layers):
             if i == cfg.late_layer_start:
                 lf = max(0, T - cfg.late_replay) if late_from is None else late_from
@@ -299,6 +302,8 @@ class RefModel:
 
     def head(self, X: torch.Tensor) -> torch.Tensor:
         cfg, w = self.cfg, self.w
+        if cfg.plain_residual:
+            return ops.rms_norm(X[:, 0], w["norm.weight"], cfg.rms_eps) @ w["head.weight"].t()
         pre = ops.mhc_head_coeffs(X, w["head_hc.fn"], w["head_hc.base"], w["head_hc.scale"], cfg.hc_eps, cfg.rms_eps)
         y = ops.rms_norm(ops.mhc_pre_mix(X, pre), w["norm.weight"], cfg.rms_eps)
         return y @ w["head.weight"].t()

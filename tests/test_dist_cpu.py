@@ -36,6 +36,8 @@ def _cfg(variant):
 
     if variant == "v4_late":
         return tiny_v4_config().replace(n_layers=3, index_sources=(1,), late_layer_start=2, late_replay=24)
+    if variant == "v3_plain":
+        return tiny_config().replace(hc_mult=0)
     return tiny_v4_config().replace(n_layers=3, index_sources=(1,)) if variant == "v4" else tiny_config()
 
 
@@ -61,7 +63,7 @@ def _worker(rank, world, port, q, attn_dp=False, variant="v3"):
 @pytest.mark.parametrize("world,attn_dp,variant", [(2, False, "v3"), (2, True, "v3"), (2, False, "v4"),
                                                    (2, True, "v4"), (2, False, "v4_late"), (2, True, "v4_late"),
                                                    (2, True, "skewed"), (2, False, "skewed"), (4, False, "v3"),
-                                                   (4, True, "v3")])
+                                                   (4, True, "v3"), (2, False, "v3_plain")])
 def test_tp_ep_engine_matches_single_rank(world, attn_dp, variant):
     cfg = _cfg(variant)
     w = init_weights(cfg, seed=0)

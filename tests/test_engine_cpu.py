@@ -11,16 +11,20 @@ from carbon_b200.ref.model import RefModel, init_weights
 import pytest
 
 
-@pytest.mark.parametrize("variant", ["v3", "v41_features", "v4_latent", "v4_latent_nodsa", "v4_image", "v4_late"])
+@pytest.mark.parametrize("variant", ["v3", "v3_plain", "v41_features", "v4_latent", "v4_latent_nodsa", "v4_image",
+                                     "v4_late"])
 def test_tiny_engine_matches_oracle(variant):
     """v41_features: DSA selection computed by index-source layers 1 and 3 only (layer 0 dense, layer 2 reuses
     layer 1's selection) and per-head attention sinks.  v4_latent: the V4 attention layout (latent MQA with output
     RoPE rotated back, grouped low-rank output projection, sliding window 16 + top-16 over older keys, sinks,
     sqrt-softplus router, Engram on layer 1); v4_latent_nodsa: the same without the indexer (window-only attention);
     v4_image: image tokens (every 5th prompt token) rank experts with the image bias and skip the Engram update;
-    v4_late: bounded late-layer replay (layer 2 runs only each prompt's last 24 tokens, window-only)."""
+    v4_late: bounded late-layer replay (layer 2 runs only each prompt's last 24 tokens, window-only); v3_plain: no
+    hyper-connections (one residual stream, x + f(norm(x)), as in DeepSeek-V3 / V3.2 checkpoints)."""
     cfg = tiny_config()
-    if variant == "v41_features":
+    if variant == "v3_plain":
+        cfg = cfg.replace(hc_mult=0, n_layers=3, n_dense_layers=1)
+    elif variant == "v41_features":
         cfg = cfg.replace(n_layers=4, index_sources=(1, 3), attn_sink=True)
     elif variant == "v4_latent":
         cfg = tiny_v4_config().replace(n_layers=3, index_sources=(1,))

@@ -269,3 +269,25 @@ def test_fp8_indexer_model_vs_oracle():
     r2 = eng.add_request(prompt.tolist() + [int(torch.argmax(got))])
     full = eng.prefill([r2])[0].float().cpu()
     assert _rel(dec, full) < 0.1, _rel(dec, full)
+
+
+def test_plain_residual_model_vs_oracle():
+    """hc_mult = 0 (no hyper-connections, the DeepSeek-V3 / V3.2 residual): RMSNorm kernel with fp8 output in front
+    of each sublayer, residual add after it; prefill against the oracle, decode against a longer prefill."""
+    cfg = _cfg().replace(hc_mult=0)
+    w = fp8_roundtrip(init_weights(cfg, seed=0))
+    ref = RefModel(cfg, w)
+    g = torch.Generator().manual_seed(5)
+    prompt = torch.randint(0, cfg.vocab_size, (200,), generator=g)
+    eng = Engine(cfg, device="cuda", source=WeightSource(cfg, state=w), num_pages=32, page_size=64)
+    eng.model.trace = []
+    r = eng.add_request(prompt.tolist())
+    got = eng.prefill([r])[0].float().cpu()
+    ref.forced_routing = {int(k.split(".")[0]): v.long() for k, v in eng.model.trace if k.endswith("router_ids")}
+    exp = ref.forward(prompt)[-1]
+    assert _rel(got, exp) < 0.15, _rel(got, exp)
+    eng.model.trace = None
+    r1 = eng.add_request(prompt[:-1].tolist())
+    eng.prefill([r1])
+    dec = eng.decode([r1], [int(prompt[-1])])[0].float().cpu()
+    assert _rel(dec, got) < 0.1, _rel(dec, got)
