@@ -13,6 +13,7 @@ from __future__ import annotations
 
 import dataclasses
 import json
+import math
 import os
 from dataclasses import dataclass, field
 from typing import Any, Dict, Optional
@@ -35,6 +36,12 @@ class ModelConfig:
     qk_rope_head_dim: int = 64
     v_head_dim: int = 128
     rope_theta: float = 10000.0
+    # YaRN context extension (DeepSeek-V3's rope_scaling): 1.0 = off
+    rope_factor: float = 1.0
+    rope_orig_max: int = 4096
+    rope_beta_fast: float = 32.0
+    rope_beta_slow: float = 1.0
+    rope_mscale_all_dim: float = 1.0
     max_position: int = 16384
     # DSA lightning indexer (0 heads => dense attention)
     index_n_heads: int = 64
@@ -96,6 +103,8 @@ class ModelConfig:
     n_shared_experts: int = 1
     moe_intermediate: int = 2048
     score_func: str = "sigmoid"        # sigmoid | sqrtsoftplus | softmax
+    n_groups: int = 1                  # group-limited routing (DeepSeek-V3: 8 groups, the best 4 by top-2 score sum)
+    topk_groups: int = 1
     route_scale: float = 2.5
     norm_topk_prob: bool = True
     swiglu_limit: float = 0.0          # 0 => no clamp
@@ -187,7 +196,18 @@ class ModelConfig:
 
     @property
     def softmax_scale(self) -> float:
-        return self.qk_head_dim ** -0.5
+        s = self.qk_head_dim ** -0.5
+        if self.rope_factor > 1.0:          # YaRN attention temperature, applied to the logits as mscale^2
+            m = 0.1 * self.rope_mscale_all_dim * math.log(self.rope_factor) + 1.0
+            s *= m * m
+        return s
+
+    @property
+    def rope(self):
+        """RoPE spec for ``ref.ops.rope_cos_sin``: theta, or (theta, factor, orig_max, beta_fast, beta_slow) with YaRN."""
+        if self.rope_factor > 1.0:
+            return (self.rope_theta, self.rope_factor, self.rope_orig_max, self.rope_beta_fast, self.rope_beta_slow)
+        return self.rope_theta
 
     # ---- construction --------------------------------------------------------------------------------------------
     @classmethod
@@ -204,6 +224,39 @@ class ModelConfig:
 
         with open(path) as f:
             return cls.from_dict(yaml.safe_load(f) or {})
+
+    @classmethod
+    def from_hf(cls, src) -> "ModelConfig":
+        """A Hugging Face DeepSeek-V3 / V3.2 ``config.json`` (a path, a directory holding one, or its dict):
+        plain residual (no hyper-connections), group-limited sigmoid routing, YaRN RoPE scaling and, for V3.2,
+        the DSA indexer.  The multi-token-prediction layers are not part of the model here."""
+        if not isinstance(src, dict):
+            path = os.path.join(src, "config.json") if os.path.isdir(src) else src
+            with open(path) as f:
+                src = json.load(f)
+        d = src
+        kw: Dict[str, Any] = dict(
+            vocab_size=d["vocab_size"], hidden_size=d["hidden_size"], n_layers=d["num_hidden_layers"],
+            n_dense_layers=d.get("first_k_dense_replace", 0), dense_intermediate=d["intermediate_size"],
+            n_heads=d["num_attention_heads"], q_lora_rank=d.get("q_lora_rank") or 0, kv_lora_rank=d["kv_lora_rank"],
+            qk_nope_head_dim=d["qk_nope_head_dim"], qk_rope_head_dim=d["qk_rope_head_dim"],
+            v_head_dim=d["v_head_dim"], rope_theta=float(d.get("rope_theta", 10000.0)),
+            max_position=d.get("max_position_embeddings", 4096),
+            n_routed_experts=d.get("n_routed_experts") or 0, n_activated_experts=d.get("num_experts_per_tok") or 0,
+            n_shared_experts=d.get("n_shared_experts") or 0, moe_intermediate=d.get("moe_intermediate_size", 0),
+            score_func=d.get("scoring_func", "softmax"), route_scale=float(d.get("routed_scaling_factor", 1.0)),
+            norm_topk_prob=bool(d.get("norm_topk_prob", False)), n_groups=d.get("n_group") or 1,
+            topk_groups=d.get("topk_group") or 1, rms_eps=float(d.get("rms_norm_eps", 1e-6)),
+            tie_word_embeddings=bool(d.get("tie_word_embeddings", False)), hc_mult=0,
+            index_n_heads=d.get("index_n_heads", 0), index_head_dim=d.get("index_head_dim", 128),
+            index_topk=d.get("index_topk", 0))
+        rs = d.get("rope_scaling") or {}
+        if rs.get("type", rs.get("rope_type")) == "yarn":
+            kw.update(rope_factor=float(rs["factor"]),
+                      rope_orig_max=int(rs.get("original_max_position_embeddings", 4096)),
+                      rope_beta_fast=float(rs.get("beta_fast", 32)), rope_beta_slow=float(rs.get("beta_slow", 1)),
+                      rope_mscale_all_dim=float(rs.get("mscale_all_dim", 1.0)))
+        return cls(**kw)
 
     def to_dict(self) -> Dict[str, Any]:
         return dataclasses.asdict(self)

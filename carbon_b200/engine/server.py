@@ -16,6 +16,7 @@ GPU) or build ``make_app(engine)`` around an engine of your own.
 """
 import argparse
 import json
+import os
 import threading
 from contextlib import asynccontextmanager
 from typing import List
@@ -146,6 +147,10 @@ def main():
     ap.add_argument("--checkpoint", default=None)
     a = ap.parse_args()
     cfg = PRESETS[a.preset]()
+    if a.checkpoint and os.path.exists(os.path.join(a.checkpoint, "config.json")):
+        from ..config import ModelConfig
+
+        cfg = ModelConfig.from_hf(a.checkpoint)           # a Hugging Face DeepSeek checkpoint directory
     if a.checkpoint:
         from ..models.checkpoint import CheckpointSource
 

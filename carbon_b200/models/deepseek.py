@@ -165,7 +165,7 @@ class DeepseekModel:
         self.E_local = cfg.n_routed_experts // ep if cfg.n_routed_experts else 0
         dev = self.device
         get = lambda n, rows=None: source.get(n, dev, rows)
-        self.cos_sin = C.rope_table(cfg.max_position, cfg.qk_rope_head_dim, cfg.rope_theta, dev)
+        self.cos_sin = C.rope_table(cfg.max_position, cfg.qk_rope_head_dim, cfg.rope, dev)
         self.act_dtype = torch.bfloat16 if self.on_gpu else torch.float32
         # vocab-parallel embedding/head: each rank keeps rows [v_lo, v_hi)
         V = cfg.vocab_size
@@ -691,7 +691,7 @@ class DeepseekModel:
             w, ids = C.router_topk(logits, L.gate_b, cfg.n_activated_experts, cfg.score_func, cfg.route_scale,
                                    cfg.norm_topk_prob, bias_img=L.gate_b_img,
                                    tok=self._tok_local if L.gate_b_img is not None else None,
-                                   img_id=cfg.image_token_id)
+                                   img_id=cfg.image_token_id, n_groups=cfg.n_groups, topk_groups=cfg.topk_groups)
         self._tr(f"{i}.router_ids", ids)
         if self.expert_load is not None:
             self.expert_load.record_device(i, ids)

@@ -35,7 +35,7 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, want_bf16: bool = Tru
 
 def rope_table(max_pos: int, dim: int, theta: float, device) -> torch.Tensor:
     """fp32 [max_pos, dim] interleaved (cos_j, sin_j) pairs computed in fp64."""
-    cos, sin = R.rope_cos_sin(torch.arange(max_pos), dim, theta)
+    cos, sin = R.rope_cos_sin(torch.arange(max_pos), dim, theta)     # theta: a float or a YaRN spec
     return torch.stack([cos, sin], dim=-1).reshape(max_pos, dim).contiguous().to(device)
 
 
@@ -59,14 +59,16 @@ def rope_(x: torch.Tensor, off: int, dim: int, table: torch.Tensor, pos: torch.T
 
 def router_topk(logits: torch.Tensor, bias: Optional[torch.Tensor], k: int, score_func: str, route_scale: float,
                 norm: bool, bias_img: Optional[torch.Tensor] = None, tok: Optional[torch.Tensor] = None,
-                img_id: int = -1) -> Tuple[torch.Tensor, torch.Tensor]:
-    """Biased top-k router; with ``bias_img``, tokens whose id (``tok``) is ``img_id`` rank with that bias."""
-    if not logits.is_cuda:
+                img_id: int = -1, n_groups: int = 1, topk_groups: int = 1) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Biased top-k router; with ``bias_img``, tokens whose id (``tok``) is ``img_id`` rank with that bias.
+    Group-limited routing (``n_groups`` > 1: experts only from the ``topk_groups`` groups with the best top-2 key
+    sums) runs as tensor ops on the logits' device; the router kernel covers ungrouped routing."""
+    if not logits.is_cuda or n_groups > 1:
         if bias_img is not None and tok is not None:
             is_img = (tok.long() == img_id)[:, None]
             b = bias if bias is not None else torch.zeros_like(bias_img)
             bias = torch.where(is_img, bias_img.float()[None, :], b.float()[None, :])
-        return R.router_topk(logits, bias, k, score_func, route_scale, norm)
+        return R.router_topk(logits, bias, k, score_func, route_scale, norm, n_groups, topk_groups)
     T = logits.shape[0]
     w = torch.empty(T, k, dtype=torch.float32, device=logits.device)
     ids = torch.empty(T, k, dtype=torch.int32, device=logits.device)

@@ -140,18 +140,18 @@ class RefModel:
             q_lat = h
             q = (h @ w[L + "wq.weight"].t()).view(T, H, dq)
         dn = dq - dr                                  # non-RoPE part of q
-        qf = torch.cat([q[..., :dn], ops.apply_rope(q[..., dn:], pos, cfg.rope_theta)], dim=-1)
+        qf = torch.cat([q[..., :dn], ops.apply_rope(q[..., dn:], pos, cfg.rope)], dim=-1)
         kv = h @ w[L + "wkv_a.weight"].t()
         if cfg.attn_kind == "latent_mqa":
             # one shared head: the normalised latent, RoPE on its last dr dims; value = the same row
             kv_c = ops.rms_norm(kv, w[L + "kv_norm.weight"], cfg.rms_eps)
-            k = torch.cat([kv_c[:, :r - dr], ops.apply_rope(kv_c[:, None, r - dr:], pos, cfg.rope_theta)[:, 0]],
+            k = torch.cat([kv_c[:, :r - dr], ops.apply_rope(kv_c[:, None, r - dr:], pos, cfg.rope)[:, 0]],
                           dim=-1)[:, None, :]                                   # [T,1,r]
             v = k
         else:
             dv = cfg.v_head_dim
             kv_c = ops.rms_norm(kv[:, :r], w[L + "kv_norm.weight"], cfg.rms_eps)
-            k_pe = ops.apply_rope(kv[:, None, r:], pos, cfg.rope_theta)         # [T,1,dr]
+            k_pe = ops.apply_rope(kv[:, None, r:], pos, cfg.rope)         # [T,1,dr]
             kvb = (kv_c @ w[L + "wkv_b.weight"].t()).view(T, H, dn + dv)
             k = torch.cat([kvb[..., :dn], k_pe.expand(T, H, dr)], dim=-1)
             v = kvb[..., dn:]
@@ -182,7 +182,7 @@ class RefModel:
         o = ops.causal_attention(qf, k, v, cfg.softmax_scale, pos, pos, allowed, sink=sink)   # [T,H,dvh]
         if cfg.attn_kind == "latent_mqa":
             # the value's RoPE dims carry each key's rotation: rotate the output back by the query position
-            o = torch.cat([o[..., :r - dr], ops.apply_rope(o[..., r - dr:], pos, cfg.rope_theta, inverse=True)],
+            o = torch.cat([o[..., :r - dr], ops.apply_rope(o[..., r - dr:], pos, cfg.rope, inverse=True)],
                           dim=-1)
         return self.out_proj(i, o)
 
@@ -207,9 +207,9 @@ class RefModel:
         L = f"layers.{i}.attn.indexer."
         T, Hi, Di, dr = h.shape[0], cfg.index_n_heads, cfg.index_head_dim, cfg.qk_rope_head_dim
         q = (q_lat @ w[L + "wq.weight"].t()).view(T, Hi, Di)
-        q = torch.cat([ops.apply_rope(q[..., :dr], pos, cfg.rope_theta), q[..., dr:]], dim=-1)
+        q = torch.cat([ops.apply_rope(q[..., :dr], pos, cfg.rope), q[..., dr:]], dim=-1)
         k = ops.layer_norm(h @ w[L + "wk.weight"].t(), w[L + "k_norm.weight"], w[L + "k_norm.bias"], 1e-6)
-        k = torch.cat([ops.apply_rope(k[:, None, :dr], pos, cfg.rope_theta)[:, 0], k[:, dr:]], dim=-1)
+        k = torch.cat([ops.apply_rope(k[:, None, :dr], pos, cfg.rope)[:, 0], k[:, dr:]], dim=-1)
         wt = (h @ w[L + "weights_proj.weight"].t()) * (Hi ** -0.5) * (Di ** -0.5)
         if cfg.index_fp4:
             q, k = ops.fake_quant_mxfp4(q), ops.fake_quant_mxfp4(k)
@@ -228,7 +228,7 @@ class RefModel:
             is_img = (self._ids.long() == cfg.image_token_id)[:, None]
             bias = torch.where(is_img, w[L + "gate.bias_img"][None, :], bias[None, :])
         wts, ids = ops.router_topk(logits, bias, cfg.n_activated_experts, cfg.score_func,
-                                   cfg.route_scale, cfg.norm_topk_prob)
+                                   cfg.route_scale, cfg.norm_topk_prob, cfg.n_groups, cfg.topk_groups)
         if self.forced_routing is not None and i in self.forced_routing:
             ids = self.forced_routing[i].to(ids.dtype)
             act = torch.sigmoid(logits) if cfg.score_func == "sigmoid" else (

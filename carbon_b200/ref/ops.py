@@ -50,8 +50,31 @@ def softplus(x: torch.Tensor) -> torch.Tensor:
 # ----------------------------------------------------------------------------------------------------------------------
 # RoPE (interleaved pairs: (x[2i], x[2i+1]) rotated by pos·θ^(-2i/d))
 # ----------------------------------------------------------------------------------------------------------------------
-def rope_cos_sin(positions: torch.Tensor, dim: int, theta: float) -> Tuple[torch.Tensor, torch.Tensor]:
+def rope_inv_freq(dim: int, rope) -> torch.Tensor:
+    """Inverse frequencies [dim/2] (fp64).  ``rope`` is theta, or (theta, factor, orig_max, beta_fast, beta_slow)
+    for YaRN (Peng et al., 2023): dimensions that turn fewer than beta_slow times over the original context are
+    interpolated (frequency / factor), those that turn more than beta_fast times are kept, with a linear ramp
+    between the two correction dimensions."""
+    theta = rope[0] if isinstance(rope, tuple) else rope
     inv = 1.0 / (theta ** (torch.arange(0, dim, 2, dtype=torch.float64) / dim))
+    if not isinstance(rope, tuple):
+        return inv
+    _, factor, orig, beta_fast, beta_slow = rope
+
+    def corr_dim(turns):                    # dimension index whose wavelength fits ``turns`` times in ``orig``
+        return dim * math.log(orig / (turns * 2 * math.pi)) / (2 * math.log(theta))
+
+    lo = max(math.floor(corr_dim(beta_fast)), 0)
+    hi = min(math.ceil(corr_dim(beta_slow)), dim - 1)
+    if lo == hi:
+        hi += 0.001
+    ramp = ((torch.arange(dim // 2, dtype=torch.float64) - lo) / (hi - lo)).clamp(0, 1)
+    keep = 1.0 - ramp                       # 1: original frequency, 0: interpolated
+    return inv / factor * (1 - keep) + inv * keep
+
+
+def rope_cos_sin(positions: torch.Tensor, dim: int, theta) -> Tuple[torch.Tensor, torch.Tensor]:
+    inv = rope_inv_freq(dim, theta)
     ang = positions.to(torch.float64)[:, None] * inv[None, :]
     return torch.cos(ang).float(), torch.sin(ang).float()
 
@@ -270,7 +293,7 @@ def router_topk(logits: torch.Tensor, bias: Optional[torch.Tensor], k: int, scor
         g = key.view(T, n_groups, E // n_groups)
         gscore = g.topk(2, dim=-1).values.sum(-1)
         keep = _stable_topk(gscore, topk_groups)
-        mask = torch.zeros(T, n_groups, dtype=torch.bool)
+        mask = torch.zeros(T, n_groups, dtype=torch.bool, device=key.device)
         mask.scatter_(1, keep, True)
         key = key.masked_fill(~mask.repeat_interleave(E // n_groups, dim=1), float("-inf"))
     ids = _stable_topk(key, k)

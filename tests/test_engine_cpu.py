@@ -11,7 +11,7 @@ from carbon_b200.ref.model import RefModel, init_weights
 import pytest
 
 
-@pytest.mark.parametrize("variant", ["v3", "v3_plain", "v41_features", "v4_latent", "v4_latent_nodsa", "v4_image",
+@pytest.mark.parametrize("variant", ["v3", "v3_plain", "v3_hf", "v41_features", "v4_latent", "v4_latent_nodsa", "v4_image",
                                      "v4_late"])
 def test_tiny_engine_matches_oracle(variant):
     """v41_features: DSA selection computed by index-source layers 1 and 3 only (layer 0 dense, layer 2 reuses
@@ -24,6 +24,8 @@ def test_tiny_engine_matches_oracle(variant):
     cfg = tiny_config()
     if variant == "v3_plain":
         cfg = cfg.replace(hc_mult=0, n_layers=3, n_dense_layers=1)
+    elif variant == "v3_hf":                # + group-limited routing and YaRN RoPE (DeepSeek-V3's config.json)
+        cfg = cfg.replace(hc_mult=0, n_groups=4, topk_groups=2, rope_factor=8.0, rope_orig_max=32)
     elif variant == "v41_features":
         cfg = cfg.replace(n_layers=4, index_sources=(1, 3), attn_sink=True)
     elif variant == "v4_latent":

@@ -273,8 +273,9 @@ def test_fp8_indexer_model_vs_oracle():
 
 def test_plain_residual_model_vs_oracle():
     """hc_mult = 0 (no hyper-connections, the DeepSeek-V3 / V3.2 residual): RMSNorm kernel with fp8 output in front
-    of each sublayer, residual add after it; prefill against the oracle, decode against a longer prefill."""
-    cfg = _cfg().replace(hc_mult=0)
+    of each sublayer, residual add after it; with group-limited routing and YaRN RoPE as in DeepSeek-V3's config.
+    Prefill against the oracle, decode against a longer prefill."""
+    cfg = _cfg().replace(hc_mult=0, n_groups=2, topk_groups=1, rope_factor=4.0, rope_orig_max=64)
     w = fp8_roundtrip(init_weights(cfg, seed=0))
     ref = RefModel(cfg, w)
     g = torch.Generator().manual_seed(5)

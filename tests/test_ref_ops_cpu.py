@@ -123,3 +123,34 @@ def test_engram_hash_rows_stay_in_their_columns():
     assert torch.allclose(R.engram_gate(X, kv, torch.ones(32), torch.ones(32), 1e-6, 10.0), X)   # zero value: no-op
     assert math.isfinite(float(R.engram_gate(X, torch.randn(4, 160, generator=g), torch.ones(32), torch.ones(32),
                                              1e-6, 10.0).sum()))
+
+
+def test_yarn_rope_and_group_limited_router():
+    from carbon_b200.config import ModelConfig
+
+    base = R.rope_inv_freq(64, 10000.0)
+    y = R.rope_inv_freq(64, (10000.0, 40.0, 4096, 32.0, 1.0))
+    ratio = y / base
+    assert torch.allclose(ratio[:8], torch.ones(8, dtype=ratio.dtype))                # fast dims kept
+    assert torch.allclose(ratio[-4:], torch.full((4,), 1 / 40, dtype=ratio.dtype))    # slow dims interpolated
+    assert (ratio[1:] <= ratio[:-1] + 1e-12).all()                                     # monotone ramp
+    cos, sin = R.rope_cos_sin(torch.arange(5), 64, 10000.0)
+    assert torch.allclose(cos ** 2 + sin ** 2, torch.ones_like(cos), atol=1e-6)
+    g = torch.Generator().manual_seed(7)
+    logits = torch.randn(64, 32, generator=g)
+    bias = torch.randn(32, generator=g) * 0.1
+    w, ids = R.router_topk(logits, bias, 6, "sigmoid", 2.5, True, n_groups=8, topk_groups=3)
+    assert all(len({int(e) // 4 for e in row}) <= 3 for row in ids)                    # experts from <= 3 groups
+    assert torch.allclose(w.sum(1), torch.full((64,), 2.5), atol=1e-5)
+    hf = {"vocab_size": 129280, "hidden_size": 7168, "intermediate_size": 18432, "moe_intermediate_size": 2048,
+          "num_hidden_layers": 61, "num_attention_heads": 128, "n_shared_experts": 1, "n_routed_experts": 256,
+          "routed_scaling_factor": 2.5, "kv_lora_rank": 512, "q_lora_rank": 1536, "qk_rope_head_dim": 64,
+          "v_head_dim": 128, "qk_nope_head_dim": 128, "n_group": 8, "topk_group": 4, "num_experts_per_tok": 8,
+          "first_k_dense_replace": 3, "norm_topk_prob": True, "scoring_func": "sigmoid", "rms_norm_eps": 1e-6,
+          "rope_theta": 10000, "max_position_embeddings": 163840,
+          "rope_scaling": {"beta_fast": 32, "beta_slow": 1, "factor": 40, "mscale": 1.0, "mscale_all_dim": 1.0,
+                           "original_max_position_embeddings": 4096, "type": "yarn"}}
+    c = ModelConfig.from_hf(hf)
+    assert c.plain_residual and c.n_groups == 8 and c.topk_groups == 4 and c.n_dense_layers == 3
+    assert abs(c.softmax_scale - 192 ** -0.5 * (0.1 * math.log(40) + 1) ** 2) < 1e-12
+    assert c.index_topk == 0 and c.rope[1] == 40.0
