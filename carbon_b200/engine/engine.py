@@ -35,6 +35,7 @@ class Request:
     n_cached: int = 0            # tokens whose KV is in the cache
     done: bool = False
     late_from: int = 0           # first position that exists at the late layers (bounded late-layer replay)
+    home: int = -1               # DP owner-only KV: the rank that caches this request's KV and runs its rows
 
     @property
     def seq_len(self) -> int:
@@ -117,7 +118,8 @@ class Engine:
     def __init__(self, cfg: ModelConfig, device="cpu", source: Optional[WeightSource] = None, num_pages: int = 256,
                  page_size: int = 64, model: Optional[DeepseekModel] = None, cuda_graphs: bool = False,
                  graph_buckets: Sequence[int] = (1, 2, 4, 8, 16, 32, 64, 128, 256), pctx=None, fp8: bool = True,
-                 prefix_cache: bool = False, record_expert_load: bool = False, balance_dp: bool = False):
+                 prefix_cache: bool = False, record_expert_load: bool = False, balance_dp: bool = False,
+                 dp_owner_kv: bool = False):
         self.cfg = cfg
         self.device = torch.device(device)
         self.model = model if model is not None else DeepseekModel(cfg, source or WeightSource(cfg), device,
@@ -140,6 +142,17 @@ class Engine:
         # each prompt's own replayed tail)
         # DP attention: place prefill sequences and decode rows on ranks by a FLOP cost model instead of by count
         self.balance_dp = balance_dp
+        # DP attention with owner-only KV: every request has a home rank (chosen by the cost-model planner at its
+        # prefill) that alone allocates and writes its KV pages; its prefill and decode rows always run there, and
+        # decode pads each rank's rows to the busiest rank's count (fixed per-rank blocks for the decode graphs).
+        # Each rank then holds only its own requests' KV (the reference's DP-attention layout).
+        pc = self.model.pctx
+        self.dp_owner_kv = bool(dp_owner_kv and pc.world > 1 and pc.attn_dp)
+        if dp_owner_kv and not self.dp_owner_kv:
+            raise ValueError("dp_owner_kv needs DP attention on several ranks")
+        if self.dp_owner_kv and prefix_cache:
+            raise ValueError("dp_owner_kv does not combine with the prefix cache (pages are per home rank)")
+        self.model.dp_owner_kv = self.dp_owner_kv
         if record_expert_load and cfg.n_routed_experts:
             from ..parallel.placement import ExpertLoad
 
@@ -171,7 +184,19 @@ class Engine:
             n += sum(1 for p in self.prefix.entries.values() if a.refcount(p) == 1)
         return n
 
+    def _mine(self, r: Request) -> bool:
+        return not self.dp_owner_kv or r.home == self.model.pctx.rank
+
+    def _table(self, r: Request, n_tokens: int) -> List[int]:
+        """Page table used for ``r``'s metadata on this rank: its pages, or (owner-only KV, another rank's request)
+        the scratch page for every position, so this rank never touches pages it does not own."""
+        if self._mine(r):
+            return r.pages
+        return [self._scratch[0]] * max(1, (n_tokens + self.page_size - 1) // self.page_size)
+
     def _ensure_pages(self, r: Request, n_tokens: int):
+        if not self._mine(r):
+            return
         need = self.pages_for(r, n_tokens)
         if need > 0:
             while self.prefix is not None and self.cache.alloc.num_free() < need and self.prefix.entries:
@@ -222,10 +247,15 @@ class Engine:
         with a cached prefix (chunked prefill, prefix reuse) continue through per-row attention over the cache."""
         if any(r.n_cached > 0 for r in reqs):
             return self._prefill_rows(reqs, [r.seq_len - r.n_cached for r in reqs])
-        if self._dp_balanced() and len(reqs) > 1:
+        if self.dp_owner_kv or (self._dp_balanced() and len(reqs) > 1):
             from ..parallel.balance import plan_prefill
 
             order, bounds, _ = plan_prefill(self.cfg, [r.seq_len for r in reqs], self.model.pctx.world)
+            if self.dp_owner_kv:                # the planned rank becomes each request's home
+                start = 0
+                for i in order:
+                    reqs[i].home = max(k for k in range(len(bounds) - 1) if bounds[k] <= start)
+                    start += reqs[i].seq_len
             logits = self._prefill_full([reqs[i] for i in order], bounds)
             inv = [0] * len(order)
             for j, i in enumerate(order):
@@ -245,7 +275,7 @@ class Engine:
         if self.cfg.late_layer_start >= 0:
             for r, n in zip(reqs, lens):
                 r.late_from = max(0, n - self.cfg.late_replay)
-        out_loc, pos = prefill_metadata([r.pages for r in reqs], starts, lens, self.page_size)
+        out_loc, pos = prefill_metadata([self._table(r, r.seq_len) for r in reqs], starts, lens, self.page_size)
         cu = [0]
         for n in lens:
             cu.append(cu[-1] + n)
@@ -288,6 +318,8 @@ class Engine:
         """Run the next ``counts[b]`` uncached tokens of each request as per-row attention over the paged cache
         (keys: the request's cached tokens and the rows before it).  Returns logits [B, V] of each request's last
         row of this step."""
+        if self.dp_owner_kv:
+            raise NotImplementedError("per-row prefill (chunks, cached prefixes) with dp_owner_kv")
         rows_pt, rows_len, ids, late, last = [], [], [], [], []
         for r, n in zip(reqs, counts):
             toks = (r.prompt + r.out)[r.n_cached:r.n_cached + n]
@@ -314,6 +346,8 @@ class Engine:
 
     def decode(self, reqs: List[Request], next_tokens: Sequence[int]) -> torch.Tensor:
         """Append one token per request and run it; returns logits [B, V]."""
+        if self.dp_owner_kv:
+            return self._decode_owner(reqs, next_tokens)
         if self._dp_balanced() and len(reqs) > 1:
             from ..parallel.balance import plan_rows, seq_cost
 
@@ -326,6 +360,51 @@ class Engine:
                 inv[i] = j
             return logits[torch.tensor(inv, dtype=torch.long, device=logits.device)]
         return self._decode(reqs, next_tokens)
+
+    def _decode_owner(self, reqs: List[Request], next_tokens: Sequence[int]) -> torch.Tensor:
+        """Owner-only KV decode: rank r's block of the batch holds the requests whose home is r, padded to the
+        largest per-rank count (pad rows read and write the scratch page), so the even split of the step's rows
+        puts every request on its home rank."""
+        pc = self.model.pctx
+        groups: List[List[int]] = [[] for _ in range(pc.world)]
+        for j, r in enumerate(reqs):
+            if not 0 <= r.home < pc.world:
+                raise RuntimeError(f"request {r.rid} has no home rank (prefill it on this engine first)")
+            groups[r.home].append(j)
+        m = max(len(g) for g in groups)
+        mb = (self._bucket(m) or m) if self.cuda_graphs else m
+        order: List[Optional[int]] = []
+        for g in groups:
+            order += g + [None] * (mb - len(g))
+        for r, t in zip(reqs, next_tokens):
+            r.out.append(int(t))
+            self._ensure_pages(r, r.seq_len)
+        total = len(order)
+        tables = [self._table(reqs[j], reqs[j].seq_len) if j is not None else [self._scratch[0]] for j in order]
+        lens = [reqs[j].seq_len if j is not None else 1 for j in order]
+        out_loc, key_slots, n_keys, pos = decode_metadata(tables, lens, self.page_size, total)
+        ids = torch.tensor([reqs[j].out[-1] if j is not None else 0 for j in order], dtype=torch.int32)
+        late = torch.tensor([reqs[j].late_from if j is not None else 0 for j in order], dtype=torch.int32)
+        st = self.stager
+        ids, pos, out_loc = st.to_device("d_ids", ids), st.to_device("d_pos", pos), st.to_device("d_loc", out_loc)
+        key_slots, n_keys = st.to_device("d_keys", key_slots), st.to_device("d_nk", n_keys)
+        late = st.to_device("d_late", late)
+        B = len(reqs)
+        with self.metrics.step("decode", B, B):
+            if self.cuda_graphs and self._bucket(m) is not None:
+                logits = self._graph(total, key_slots.shape[1]).run(ids, pos, out_loc, key_slots, n_keys, late)
+            else:
+                fb = ForwardBatch(ids=ids, pos=pos, out_loc=out_loc, is_prefill=False, key_slots=key_slots,
+                                  n_keys=n_keys, bounds=self._bounds([1] * total), late_from=late)
+                logits = self.model.forward(fb, self.cache)
+        where = [0] * B
+        for k, j in enumerate(order):
+            if j is not None:
+                where[j] = k
+        for r in reqs:
+            r.n_cached = r.seq_len
+        self.stats["decode_tokens"] += B
+        return logits[torch.tensor(where, dtype=torch.long, device=logits.device)]
 
     def _decode(self, reqs: List[Request], next_tokens: Sequence[int]) -> torch.Tensor:
         B = len(reqs)
@@ -363,6 +442,8 @@ class Engine:
         attending to the cache plus the rows before it. Greedy acceptance keeps the longest draft prefix the target
         agrees with and adds the target's next token. Returns the accepted new tokens per request (>= 1 each).
         KV rows of rejected drafts are simply overwritten later (positions are slot-addressed)."""
+        if self.dp_owner_kv:
+            raise NotImplementedError("speculative verify with dp_owner_kv")
         rows_pt, rows_len, ids, late = [], [], [], []
         for r, t, d in zip(reqs, last_tokens, drafts):
             base = r.seq_len

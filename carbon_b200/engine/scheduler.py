@@ -61,6 +61,9 @@ class Scheduler:
         """heartbeat (``utils.health.Heartbeat``): checked before every step, so a dead peer stops this rank before
         it launches work that would wait for it; watchdog (``utils.health.Watchdog``): a step that overruns its
         limit raises ``StepStalled``; check_device: read the cross-rank kernels' status word after every step."""
+        if getattr(engine, "dp_owner_kv", False):
+            raise NotImplementedError("the scheduler's page accounting assumes every rank holds every request's KV; "
+                                      "drive a dp_owner_kv engine through prefill / decode / generate")
         self.eng = engine
         self.heartbeat = heartbeat
         self.watchdog = watchdog

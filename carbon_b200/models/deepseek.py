@@ -155,6 +155,7 @@ class DeepseekModel:
         self.fp8 = fp8
         self.trace = None          # set to a list to record (name, tensor) at sublayer boundaries (debugging)
         self.expert_load = None    # placement.ExpertLoad: per-layer routing counts for expert rebalancing
+        self.dp_owner_kv = False   # DP attention: only a request's home rank caches its KV (no all-gather)
         self._side = None          # side stream of the shared expert
         self._dsa = {}
         cfg.validate()
@@ -447,7 +448,13 @@ class DeepseekModel:
             with region("attn.indexer_qk"):
                 idx_l = self.indexer_qkw(i, h, q_lat_l, pos_l)
         q_lat_a = q_lat_l.to(self.act_dtype) if self.on_gpu else q_lat_l
-        if dp:
+        out_loc = fb.out_loc
+        if dp and self.dp_owner_kv:
+            # each request's rows always run on its home rank: this rank caches only its own rows
+            q_lat, latent, latent_c = q_lat_a, latent_l, latent_l
+            idx_k = idx_l[1] if idx_l is not None else None
+            out_loc = fb.out_loc[lo:hi]
+        elif dp:
             q_lat, latent = q_lat_a, latent_l
             # every rank's cache receives every token's rows (one all-gather of the new rows): a later step may
             # give a request to another rank (prefill shards by tokens, decode by rows)
@@ -460,7 +467,6 @@ class DeepseekModel:
                 latent = pc.gather_rows(latent_l)
                 idx_k = pc.gather_rows(idx_l[1]) if idx_l is not None else None
             latent_c = latent
-        out_loc = fb.out_loc
         with region("attn.kv_proj"):
             cache.write_latent(i, out_loc, latent_c)
             if idx_k is not None:

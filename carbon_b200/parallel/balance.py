@@ -11,8 +11,9 @@ Here the cost of a sequence is counted in FLOPs from the model config (row-local
 query-key pairs per layer with the DSA top-k / window caps, indexer pairs on indexer layers), and requests are
 placed whole: LPT (longest-processing-time first) over ranks for prefill, where the per-rank token bounds follow the
 plan; and, for decode, a capacity-constrained LPT that keeps the per-rank row counts (so captured decode graphs keep
-their shapes) and only chooses which rows each rank runs.  Decode KV is in every DP rank's cache (new rows are
-all-gathered), so a request can move between ranks from one step to the next at no transfer cost.
+their shapes) and only chooses which rows each rank runs.  By default decode KV is in every DP rank's cache (new
+rows are all-gathered), so a request can move between ranks from one step to the next at no transfer cost; with
+owner-only KV (``Engine(dp_owner_kv=True)``) the prefill plan fixes each request's home rank instead.
 """
 from __future__ import annotations
 

@@ -113,3 +113,83 @@ def test_balanced_dp_engine_serves_the_same_tokens():
         assert out0 == out1, (r0, out0, out1)
         for a, b in zip(h0, h1):
             assert (torch.tensor(a) - torch.tensor(b)).abs().max() < 1e-3
+
+
+def _owner_worker(rank, world, port, q):
+    import os
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from carbon_b200.engine.engine import Engine
+    from carbon_b200.models.weights import WeightSource
+    from carbon_b200.parallel.dist import DistCtx
+    from carbon_b200.ref.model import init_weights
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    try:
+        cfg = tiny_config()
+        w = init_weights(cfg, seed=0)
+        e = Engine(cfg, device="cpu", source=WeightSource(cfg, state=w), num_pages=48, page_size=16,
+                   pctx=DistCtx(rank, world, attn_dp=True), dp_owner_kv=True)
+        reqs = [e.add_request(p) for p in _prompts(cfg)]
+        logits = e.prefill(reqs)
+        hist = [logits.tolist()]
+        nxt = torch.argmax(logits, -1).tolist()
+        outs = [[t] for t in nxt]
+        used = 0
+        for _ in range(4):
+            logits = e.decode(reqs, nxt)
+            hist.append(logits.tolist())
+            nxt = torch.argmax(logits, -1).tolist()
+            for o, t in zip(outs, nxt):
+                o.append(t)
+            used = 47 - e.cache.alloc.num_free()
+        homes = [r.home for r in reqs]
+        mine = sum(len(r.pages) for r in reqs)
+        for r in reqs:
+            e.release(r)
+        q.put((rank, outs, hist, homes, mine, used, e.cache.alloc.num_free()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_dp_owner_kv_matches_single_rank_and_splits_pages():
+    """Owner-only KV (2 DP ranks): each request's KV lives on its home rank only, yet the served tokens and logits
+    equal the single-rank engine's; the ranks' page counts add up to the single rank's."""
+    import torch.multiprocessing as mp
+
+    from carbon_b200.engine.engine import Engine
+    from carbon_b200.models.weights import WeightSource
+    from carbon_b200.ref.model import init_weights
+
+    cfg = tiny_config()
+    w = init_weights(cfg, seed=0)
+    single = Engine(cfg, device="cpu", source=WeightSource(cfg, state=w), num_pages=48, page_size=16)
+    ref_out, ref_hist = single.generate(_prompts(cfg), 5, return_logits=True)
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_owner_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda x: x[0])
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    total_pages = 0
+    for rank, outs, hist, homes, mine, used, free_after in res:
+        assert outs == ref_out, (rank, outs, ref_out)
+        for a, b in zip(hist, ref_hist):
+            assert (torch.tensor(a) - b).abs().max() < 1e-3
+        assert sorted(set(homes)) == [0, 1]                         # both ranks own requests
+        assert used == mine                                          # pages only for this rank's own requests
+        assert free_after == 47
+        total_pages += mine
+    lens = [len(p) + 4 for p in _prompts(cfg)]                      # prompt + 4 decoded tokens cached
+    assert total_pages == sum((n + 15) // 16 for n in lens)         # the KV of each request is held once
