@@ -68,7 +68,8 @@ def router_topk(logits: torch.Tensor, bias: Optional[torch.Tensor], k: int, scor
             is_img = (tok.long() == img_id)[:, None]
             b = bias if bias is not None else torch.zeros_like(bias_img)
             bias = torch.where(is_img, bias_img.float()[None, :], b.float()[None, :])
-        return R.router_topk(logits, bias, k, score_func, route_scale, norm, n_groups, topk_groups)
+        w, ids = R.router_topk(logits, bias, k, score_func, route_scale, norm, n_groups, topk_groups)
+        return w.contiguous(), ids.contiguous()          # the expert kernels read dense [T, k] rows
     T = logits.shape[0]
     w = torch.empty(T, k, dtype=torch.float32, device=logits.device)
     ids = torch.empty(T, k, dtype=torch.int32, device=logits.device)
