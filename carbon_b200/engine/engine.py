@@ -36,6 +36,7 @@ class Request:
     done: bool = False
     late_from: int = 0           # first position that exists at the late layers (bounded late-layer replay)
     home: int = -1               # DP owner-only KV: the rank that caches this request's KV and runs its rows
+    n_pages: int = 0             # DP owner-only KV: pages its home rank holds (known on every rank)
 
     @property
     def seq_len(self) -> int:
@@ -130,6 +131,7 @@ class Engine:
         self._scratch = self.cache.alloc.alloc(1)
         self.page_size = page_size
         self._next_id = 0
+        self._live: Dict[int, Request] = {}          # requests added and not yet released
         self.cuda_graphs = cuda_graphs and self.device.type == "cuda"
         self.graph_buckets = sorted(graph_buckets)
         self._graphs: Dict[int, "_DecodeGraph"] = {}
@@ -167,17 +169,24 @@ class Engine:
     def add_request(self, prompt: Sequence[int]) -> Request:
         r = Request(self._next_id, list(int(t) for t in prompt))
         self._next_id += 1
+        self._live[r.rid] = r
         if self.prefix is not None:
             r.pages = self.prefix.match(r.prompt)          # shared pages of the longest cached prefix
             r.n_cached = len(r.pages) * self.page_size
         return r
 
     def pages_for(self, r: Request, n_tokens: int) -> int:
-        """New KV pages request ``r`` needs to hold ``n_tokens`` tokens."""
-        return max(0, (n_tokens + self.page_size - 1) // self.page_size - len(r.pages))
+        """New KV pages request ``r`` needs to hold ``n_tokens`` tokens (on its home rank, with owner-only KV)."""
+        held = r.n_pages if self.dp_owner_kv else len(r.pages)
+        return max(0, (n_tokens + self.page_size - 1) // self.page_size - held)
 
-    def pages_available(self) -> int:
-        """Pages an allocation can get now: free pages plus cached prefix pages that only the prefix cache holds."""
+    def pages_available(self, home: Optional[int] = None) -> int:
+        """Pages an allocation can get now: free pages plus cached prefix pages that only the prefix cache holds.
+        With owner-only KV, the free pages of rank ``home``, counted from the page counts of the requests it owns
+        (the same number on every rank, so every rank takes the same scheduling decisions)."""
+        if self.dp_owner_kv:
+            held = sum(r.n_pages for r in self._live.values() if r.home == home)
+            return self.cache.alloc.num_pages() - 1 - held
         a = self.cache.alloc
         n = a.num_free()
         if self.prefix is not None:
@@ -195,7 +204,11 @@ class Engine:
         return [self._scratch[0]] * max(1, (n_tokens + self.page_size - 1) // self.page_size)
 
     def _ensure_pages(self, r: Request, n_tokens: int):
-        if not self._mine(r):
+        if self.dp_owner_kv:
+            need = self.pages_for(r, n_tokens)
+            if need > 0 and self._mine(r):
+                r.pages += list(self.cache.alloc.alloc(need))
+            r.n_pages += need
             return
         need = self.pages_for(r, n_tokens)
         if need > 0:
@@ -236,6 +249,8 @@ class Engine:
         if r.pages:
             self.cache.alloc.free(r.pages)
             r.pages = []
+        r.n_pages = 0
+        self._live.pop(r.rid, None)
 
     # -- steps ---------------------------------------------------------------------------------------------------------
     def _dp_balanced(self) -> bool:
@@ -250,7 +265,18 @@ class Engine:
         if self.dp_owner_kv or (self._dp_balanced() and len(reqs) > 1):
             from ..parallel.balance import plan_prefill
 
-            order, bounds, _ = plan_prefill(self.cfg, [r.seq_len for r in reqs], self.model.pctx.world)
+            world = self.model.pctx.world
+            if self.dp_owner_kv and all(r.home >= 0 for r in reqs):      # homes chosen by the caller (scheduler)
+                order = sorted(range(len(reqs)), key=lambda i: (reqs[i].home, i))
+                bounds = [0]
+                for h in range(world):
+                    bounds.append(bounds[-1] + sum(r.seq_len for r in reqs if r.home == h))
+                logits = self._prefill_full([reqs[i] for i in order], bounds)
+                inv = [0] * len(order)
+                for j, i in enumerate(order):
+                    inv[i] = j
+                return logits[torch.tensor(inv, dtype=torch.long, device=logits.device)]
+            order, bounds, _ = plan_prefill(self.cfg, [r.seq_len for r in reqs], world)
             if self.dp_owner_kv:                # the planned rank becomes each request's home
                 start = 0
                 for i in order:

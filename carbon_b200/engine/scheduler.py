@@ -9,7 +9,8 @@ several steps, every chunk attending to its cached prefix) or decodes one token 
 disaggregated prefill role; finished requests release their KV pages at once.  Admission waits for free KV pages
 (keeping one page of headroom per running request); when a decode step would run out of pages, the youngest
 requests are preempted by recompute: their pages are freed, they rejoin the queue first and, on readmission,
-prefill their prompt plus the tokens they already generated (a prefix-cache hit when enabled) and continue.  Greedy sampling, or temperature /
+prefill their prompt plus the tokens they already generated (a prefix-cache hit when enabled) and continue.
+With DP owner-only KV the same loop budgets pages per home rank (see ``_step_owner``).  Greedy sampling, or temperature /
 top-k sampling with a per-request seed.  On several ranks every rank runs the same scheduler on the same
 submissions (SPMD), so all ranks take the same steps.
 """
@@ -61,10 +62,12 @@ class Scheduler:
         """heartbeat (``utils.health.Heartbeat``): checked before every step, so a dead peer stops this rank before
         it launches work that would wait for it; watchdog (``utils.health.Watchdog``): a step that overruns its
         limit raises ``StepStalled``; check_device: read the cross-rank kernels' status word after every step."""
-        if getattr(engine, "dp_owner_kv", False):
-            raise NotImplementedError("the scheduler's page accounting assumes every rank holds every request's KV; "
-                                      "drive a dp_owner_kv engine through prefill / decode / generate")
         self.eng = engine
+        # DP attention with owner-only KV: each admitted request gets a home rank (the one with the most free
+        # pages), pages are budgeted per home rank, prompts are prefilled whole, and preemption picks its victims
+        # among the requests of the rank that runs short.  Every rank computes the same decisions.
+        self.owner = bool(getattr(engine, "dp_owner_kv", False))
+        self.world = engine.model.pctx.world
         self.heartbeat = heartbeat
         self.watchdog = watchdog
         self.check_device = check_device
@@ -131,6 +134,8 @@ class Scheduler:
         self.preemptions += 1
 
     def _step(self) -> None:
+        if self.owner:
+            return self._step_owner()
         eng = self.eng
         budget = self.prefill_tokens
         reserve = len(self.running)                 # headroom: one new page per running decode
@@ -204,6 +209,61 @@ class Scheduler:
             if not victims:
                 raise RuntimeError("KV cache too small for the running request")
             self._retract(victims[0])
+        self.steps["decode"] += 1
+        run, self.running = self.running, []
+        logits = eng.decode([j.req for j in run], [j.pending for j in run])
+        for j, row in zip(run, logits):
+            self._take(j, j.sample(row))
+
+    def _step_owner(self) -> None:
+        eng, world = self.eng, self.world
+        budget = self.prefill_tokens
+        reserve = [sum(1 for j in self.running if j.req.home == h) for h in range(world)]
+        committed = [0] * world
+        batch: List[Job] = []
+        while self.waiting and len(self.running) + len(batch) + 1 <= self.max_running:
+            j = self.waiting[0]
+            if batch and len(j.tokens()) > budget:
+                break                                   # whole prompts only: the next step takes it
+            free = [eng.pages_available(h) - reserve[h] - committed[h] for h in range(world)]
+            home = max(range(world), key=lambda h: (free[h], -h))
+            req = eng.add_request(j.tokens())
+            need = eng.pages_for(req, req.seq_len)
+            if need > free[home]:
+                eng.release(req)
+                break
+            req.home = home
+            self.waiting.popleft()
+            j.req, j.admit = req, self._admits
+            self._admits += 1
+            committed[home] += need
+            batch.append(j)
+            budget -= req.seq_len
+        if batch:
+            self.steps["prefill"] += 1
+            logits = eng.prefill([j.req for j in batch])
+            for j, row in zip(batch, logits):
+                if j.out:                               # resumed after a preemption: already sampled
+                    j.pending = j.out[-1]
+                    self.running.append(j)
+                else:
+                    self._take(j, j.sample(row))
+            return
+        if not self.running:
+            if self.waiting:
+                raise RuntimeError("KV cache too small for the next request")
+            return
+        oldest = min(self.running, key=lambda j: j.admit)           # always keeps making progress
+        for h in range(world):
+            while True:
+                mine = [j for j in self.running if j.req.home == h]
+                need = sum(eng.pages_for(j.req, j.req.seq_len + 1) for j in mine)
+                if need <= eng.pages_available(h):
+                    break
+                victims = sorted((j for j in mine if j is not oldest), key=lambda j: -j.admit)
+                if not victims:
+                    raise RuntimeError(f"KV cache of rank {h} too small for its running request")
+                self._retract(victims[0])
         self.steps["decode"] += 1
         run, self.running = self.running, []
         logits = eng.decode([j.req for j in run], [j.pending for j in run])

@@ -193,3 +193,74 @@ def test_dp_owner_kv_matches_single_rank_and_splits_pages():
         total_pages += mine
     lens = [len(p) + 4 for p in _prompts(cfg)]                      # prompt + 4 decoded tokens cached
     assert total_pages == sum((n + 15) // 16 for n in lens)         # the KV of each request is held once
+
+
+def _owner_sched_worker(rank, world, port, q, num_pages):
+    import os
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from carbon_b200.engine.engine import Engine
+    from carbon_b200.engine.scheduler import Scheduler
+    from carbon_b200.models.weights import WeightSource
+    from carbon_b200.parallel.dist import DistCtx
+    from carbon_b200.ref.model import init_weights
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+    try:
+        cfg = tiny_config()
+        w = init_weights(cfg, seed=0)
+        e = Engine(cfg, device="cpu", source=WeightSource(cfg, state=w), num_pages=num_pages, page_size=16,
+                   pctx=DistCtx(rank, world, attn_dp=True), dp_owner_kv=True)
+        s = Scheduler(e, prefill_tokens=4096)
+        ids = [s.submit(p, 40) for p in _sched_prompts(cfg)]
+        out = s.run()
+        q.put((rank, [out[i] for i in ids], s.preemptions, e.cache.alloc.num_free()))
+    finally:
+        dist.destroy_process_group()
+
+
+def _sched_prompts(cfg):
+    return [((torch.arange(30) * (k + 3) + k) % cfg.vocab_size).tolist() for k in range(4)]
+
+
+def test_scheduler_with_dp_owner_kv_under_pressure():
+    """The serving loop over 2 DP ranks with owner-only KV: homes chosen at admission, pages budgeted per rank.
+    With a per-rank cache too small for its two requests' final footprint, the ranks preempt in step (same
+    decisions on both) and every request still gets the single-rank engine's tokens."""
+    import torch.multiprocessing as mp
+
+    from carbon_b200.engine.engine import Engine
+    from carbon_b200.engine.scheduler import Scheduler
+    from carbon_b200.models.weights import WeightSource
+    from carbon_b200.ref.model import init_weights
+
+    cfg = tiny_config()
+    w = init_weights(cfg, seed=0)
+    eng = Engine(cfg, "cpu", source=WeightSource(cfg, state=w), num_pages=64, page_size=16)
+    s = Scheduler(eng)
+    ids = [s.submit(p, 40) for p in _sched_prompts(cfg)]
+    out = s.run()
+    ref = [out[i] for i in ids]
+    for num_pages, pressured in ((64, False), (9, True)):
+        sk = socket.socket()
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+        sk.close()
+        ctx = mp.get_context("spawn")
+        q = ctx.Queue()
+        ps = [ctx.Process(target=_owner_sched_worker, args=(r, 2, port, q, num_pages)) for r in range(2)]
+        for p in ps:
+            p.start()
+        res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda x: x[0])
+        for p in ps:
+            p.join(timeout=60)
+            assert p.exitcode == 0
+        for rank, got, pre, free in res:
+            assert got == ref, (num_pages, rank)
+            assert (pre > 0) == pressured, (num_pages, rank, pre)
+            assert free == num_pages - 1                          # every page back
+        assert res[0][2] == res[1][2]                             # the same preemptions on both ranks
