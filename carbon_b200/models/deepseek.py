@@ -400,7 +400,7 @@ class DeepseekModel:
 
     def plain_add(self, X, out):
         """x + f(x): the sublayer output joins the single residual stream."""
-        return X + out.to(X.dtype).view(X.shape[0], 1, X.shape[2])
+        return X + out.to(X.dtype).reshape(X.shape[0], 1, X.shape[2])
 
     def post_mix(self, X, out, post, comb):
         if not self.on_gpu:
