@@ -115,6 +115,14 @@ def prefill_metadata(page_tables, starts, lens, page_size):
     return [torch.tensor(ol, dtype=torch.int32), torch.tensor(ps, dtype=torch.int32)]
 
 
+def _unpermute(rows: torch.Tensor, order: Sequence[int]) -> torch.Tensor:
+    """rows[j] belongs to original item order[j]; returns them in original order."""
+    inv = [0] * len(order)
+    for j, i in enumerate(order):
+        inv[i] = j
+    return rows[torch.tensor(inv, dtype=torch.long, device=rows.device)]
+
+
 class Engine:
     def __init__(self, cfg: ModelConfig, device="cpu", source: Optional[WeightSource] = None, num_pages: int = 256,
                  page_size: int = 64, model: Optional[DeepseekModel] = None, cuda_graphs: bool = False,
@@ -140,8 +148,6 @@ class Engine:
 
         self.metrics = Metrics()       # device-timed steps: summary(), json_line(), prometheus()
         self.stager = PinnedStager(self.device)
-        # prefix reuse of full prompt pages (off with bounded late-layer replay: the late layers hold KV only for
-        # each prompt's own replayed tail)
         # DP attention: place prefill sequences and decode rows on ranks by a FLOP cost model instead of by count
         self.balance_dp = balance_dp
         # DP attention with owner-only KV: every request has a home rank (chosen by the cost-model planner at its
@@ -159,6 +165,8 @@ class Engine:
             from ..parallel.placement import ExpertLoad
 
             self.model.expert_load = ExpertLoad(cfg.n_routed_experts)
+        # prefix reuse of full prompt pages (off with bounded late-layer replay: the late layers hold KV only for
+        # each prompt's own replayed tail)
         self.prefix = None
         if prefix_cache and cfg.late_layer_start < 0:
             from .prefix_cache import PrefixCache
@@ -271,22 +279,14 @@ class Engine:
                 bounds = [0]
                 for h in range(world):
                     bounds.append(bounds[-1] + sum(r.seq_len for r in reqs if r.home == h))
-                logits = self._prefill_full([reqs[i] for i in order], bounds)
-                inv = [0] * len(order)
-                for j, i in enumerate(order):
-                    inv[i] = j
-                return logits[torch.tensor(inv, dtype=torch.long, device=logits.device)]
+                return _unpermute(self._prefill_full([reqs[i] for i in order], bounds), order)
             order, bounds, _ = plan_prefill(self.cfg, [r.seq_len for r in reqs], world)
             if self.dp_owner_kv:                # the planned rank becomes each request's home
                 start = 0
                 for i in order:
                     reqs[i].home = max(k for k in range(len(bounds) - 1) if bounds[k] <= start)
                     start += reqs[i].seq_len
-            logits = self._prefill_full([reqs[i] for i in order], bounds)
-            inv = [0] * len(order)
-            for j, i in enumerate(order):
-                inv[i] = j
-            return logits[torch.tensor(inv, dtype=torch.long, device=logits.device)]
+            return _unpermute(self._prefill_full([reqs[i] for i in order], bounds), order)
         return self._prefill_full(reqs, None)
 
     def _prefill_full(self, reqs: List[Request], bounds: Optional[List[int]]) -> torch.Tensor:
@@ -380,11 +380,7 @@ class Engine:
             n = self._bucket(len(reqs)) if self.cuda_graphs else len(reqs)
             n = n if n is not None else len(reqs)
             perm = plan_rows([seq_cost(self.cfg, 1, r.seq_len) for r in reqs], self._bounds([1] * n))
-            logits = self._decode([reqs[i] for i in perm], [next_tokens[i] for i in perm])
-            inv = [0] * len(perm)
-            for j, i in enumerate(perm):
-                inv[i] = j
-            return logits[torch.tensor(inv, dtype=torch.long, device=logits.device)]
+            return _unpermute(self._decode([reqs[i] for i in perm], [next_tokens[i] for i in perm]), perm)
         return self._decode(reqs, next_tokens)
 
     def _decode_owner(self, reqs: List[Request], next_tokens: Sequence[int]) -> torch.Tensor:
