@@ -343,30 +343,59 @@ class Engine:
     def _prefill_rows(self, reqs: List[Request], counts: List[int]) -> torch.Tensor:
         """Run the next ``counts[b]`` uncached tokens of each request as per-row attention over the paged cache
         (keys: the request's cached tokens and the rows before it).  Returns logits [B, V] of each request's last
-        row of this step."""
-        if self.dp_owner_kv:
-            raise NotImplementedError("per-row prefill (chunks, cached prefixes) with dp_owner_kv")
-        rows_pt, rows_len, ids, late, last = [], [], [], [], []
-        for r, n in zip(reqs, counts):
+        row of this step.  With owner-only KV the rows are grouped by home rank (requests without one get it from
+        the cost-model plan) and each rank's block is padded to the busiest rank's row count."""
+        rows_pt, rows_len, ids, late, last = [], [], [], [], [0] * len(reqs)
+
+        def add_rows(b):
+            r, n = reqs[b], counts[b]
             toks = (r.prompt + r.out)[r.n_cached:r.n_cached + n]
             self._ensure_pages(r, r.n_cached + n)
+            table = self._table(r, r.n_cached + n)
             for j, tok in enumerate(toks):
-                rows_pt.append(r.pages)
+                rows_pt.append(table)
                 rows_len.append(r.n_cached + j + 1)
                 ids.append(int(tok))
                 late.append(r.late_from)
-            last.append(len(ids) - 1)
+            last[b] = len(ids) - 1
+
+        if self.dp_owner_kv:
+            world = self.model.pctx.world
+            fresh = [b for b, r in enumerate(reqs) if r.home < 0]
+            if fresh:
+                from ..parallel.balance import plan_prefill
+
+                order, bounds, _ = plan_prefill(self.cfg, [counts[b] for b in fresh], world,
+                                                [reqs[b].n_cached for b in fresh])
+                start = 0
+                for i in order:
+                    reqs[fresh[i]].home = max(k for k in range(world) if bounds[k] <= start)
+                    start += counts[fresh[i]]
+            groups = [[b for b, r in enumerate(reqs) if r.home == h] for h in range(world)]
+            width = max(sum(counts[b] for b in g) for g in groups)
+            for g in groups:
+                k0 = len(ids)
+                for b in g:
+                    add_rows(b)
+                pad = width - (len(ids) - k0)
+                rows_pt += [[self._scratch[0]]] * pad
+                rows_len += [1] * pad
+                ids += [0] * pad
+                late += [0] * pad
+        else:
+            for b in range(len(reqs)):
+                add_rows(b)
         m = len(ids)
         out_loc, key_slots, n_keys, pos = decode_metadata(rows_pt, rows_len, self.page_size, m)
         dev = self.device
         fb = ForwardBatch(ids=torch.tensor(ids, dtype=torch.int32).to(dev), pos=pos.to(dev), out_loc=out_loc.to(dev),
                           is_prefill=False, key_slots=key_slots.to(dev), n_keys=n_keys.to(dev),
                           bounds=self._bounds([1] * m), late_from=torch.tensor(late, dtype=torch.int32).to(dev))
-        with self.metrics.step("prefill", m, len(reqs)):
+        with self.metrics.step("prefill", sum(counts), len(reqs)):
             logits = self.model.forward(fb, self.cache)
         for r, n in zip(reqs, counts):
             r.n_cached += n
-        self.stats["prefill_tokens"] += m
+        self.stats["prefill_tokens"] += sum(counts)
         self._register_prefix(reqs)
         return logits[torch.tensor(last, dtype=torch.long, device=logits.device)]
 

@@ -10,7 +10,8 @@ disaggregated prefill role; finished requests release their KV pages at once.  A
 (keeping one page of headroom per running request); when a decode step would run out of pages, the youngest
 requests are preempted by recompute: their pages are freed, they rejoin the queue first and, on readmission,
 prefill their prompt plus the tokens they already generated (a prefix-cache hit when enabled) and continue.
-With DP owner-only KV the same loop budgets pages per home rank (see ``_step_owner``).  Greedy sampling, or temperature /
+With DP owner-only KV the same loop budgets pages per home rank (each request's home: the rank with the most free
+pages at admission).  Greedy sampling, or temperature /
 top-k sampling with a per-request seed.  On several ranks every rank runs the same scheduler on the same
 submissions (SPMD), so all ranks take the same steps.
 """
@@ -64,8 +65,8 @@ class Scheduler:
         limit raises ``StepStalled``; check_device: read the cross-rank kernels' status word after every step."""
         self.eng = engine
         # DP attention with owner-only KV: each admitted request gets a home rank (the one with the most free
-        # pages), pages are budgeted per home rank, prompts are prefilled whole, and preemption picks its victims
-        # among the requests of the rank that runs short.  Every rank computes the same decisions.
+        # pages), pages are budgeted per home rank, and preemption picks its victims among the requests of the
+        # rank that runs short.  Every rank computes the same decisions.
         self.owner = bool(getattr(engine, "dp_owner_kv", False))
         self.world = engine.model.pctx.world
         self.heartbeat = heartbeat
@@ -134,12 +135,21 @@ class Scheduler:
         self.preemptions += 1
 
     def _step(self) -> None:
-        if self.owner:
-            return self._step_owner()
         eng = self.eng
+        # page budgets: one domain, or (owner-only KV) one per home rank, computed identically on every rank
+        doms = self.world if self.owner else 1
+
+        def dom(req) -> int:
+            return req.home if self.owner else 0
+
+        def avail(h: int) -> int:
+            return eng.pages_available(h) if self.owner else eng.pages_available()
+
         budget = self.prefill_tokens
-        reserve = len(self.running)                 # headroom: one new page per running decode
-        committed = 0
+        reserve = [0] * doms                        # headroom: one new page per running decode
+        for j in self.running:
+            reserve[dom(j.req)] += 1
+        committed = [0] * doms
         batch: List[Job] = []
         counts: List[int] = []
         # continue chunked prefills first, then admit new requests while the token budget, the batch size and the
@@ -148,25 +158,30 @@ class Scheduler:
             if budget <= 0:
                 break
             n = min(budget, j.req.seq_len - j.req.n_cached)
+            h = dom(j.req)
             need = eng.pages_for(j.req, j.req.n_cached + n)
-            if need > eng.pages_available() - reserve - committed:
+            if need > avail(h) - reserve[h] - committed[h]:
                 break
-            committed += need
+            committed[h] += need
             batch.append(j)
             counts.append(n)
             budget -= n
         while self.waiting and budget > 0 and len(self.running) + len(self.prefilling) + 1 <= self.max_running:
             j = self.waiting[0]
             req = eng.add_request(j.tokens())
+            if self.owner:                          # home: the rank with the most free pages
+                free = [avail(h) - reserve[h] - committed[h] for h in range(doms)]
+                req.home = max(range(doms), key=lambda h: (free[h], -h))
+            h = dom(req)
             n = min(budget, req.seq_len - req.n_cached)     # a cached prefix (prefix reuse) is skipped
             need = eng.pages_for(req, req.n_cached + n)
-            if need > eng.pages_available() - reserve - committed:
+            if need > avail(h) - reserve[h] - committed[h]:
                 eng.release(req)                            # give back the shared prefix pages
                 break
             self.waiting.popleft()
             j.req, j.admit = req, self._admits
             self._admits += 1
-            committed += need
+            committed[h] += need
             self.prefilling.append(j)
             batch.append(j)
             counts.append(n)
@@ -192,77 +207,23 @@ class Scheduler:
                         self._take(j, j.sample(row))
             return
         if not self.running:
-            if self.prefilling:                     # chunked prefills that cannot all fit: retract the youngest
-                if len(self.prefilling) > 1:
-                    self._retract(max(self.prefilling, key=lambda j: j.admit))
-                    return
+            if len(self.prefilling) > 1:            # chunked prefills that cannot all fit: retract the youngest
+                self._retract(max(self.prefilling, key=lambda j: j.admit))
+                return
             if self.waiting or self.prefilling:
                 raise RuntimeError("KV cache too small for the next request")
             return
-        # decode every running job; if the pages for this step are short, preempt the youngest jobs first
-        while True:
-            need = sum(eng.pages_for(j.req, j.req.seq_len + 1) for j in self.running)
-            if need <= eng.pages_available():
-                break
-            oldest = min(self.running, key=lambda j: j.admit)      # always keeps making progress
-            victims = sorted((j for j in self.running + self.prefilling if j is not oldest), key=lambda j: -j.admit)
-            if not victims:
-                raise RuntimeError("KV cache too small for the running request")
-            self._retract(victims[0])
-        self.steps["decode"] += 1
-        run, self.running = self.running, []
-        logits = eng.decode([j.req for j in run], [j.pending for j in run])
-        for j, row in zip(run, logits):
-            self._take(j, j.sample(row))
-
-    def _step_owner(self) -> None:
-        eng, world = self.eng, self.world
-        budget = self.prefill_tokens
-        reserve = [sum(1 for j in self.running if j.req.home == h) for h in range(world)]
-        committed = [0] * world
-        batch: List[Job] = []
-        while self.waiting and len(self.running) + len(batch) + 1 <= self.max_running:
-            j = self.waiting[0]
-            if batch and len(j.tokens()) > budget:
-                break                                   # whole prompts only: the next step takes it
-            free = [eng.pages_available(h) - reserve[h] - committed[h] for h in range(world)]
-            home = max(range(world), key=lambda h: (free[h], -h))
-            req = eng.add_request(j.tokens())
-            need = eng.pages_for(req, req.seq_len)
-            if need > free[home]:
-                eng.release(req)
-                break
-            req.home = home
-            self.waiting.popleft()
-            j.req, j.admit = req, self._admits
-            self._admits += 1
-            committed[home] += need
-            batch.append(j)
-            budget -= req.seq_len
-        if batch:
-            self.steps["prefill"] += 1
-            logits = eng.prefill([j.req for j in batch])
-            for j, row in zip(batch, logits):
-                if j.out:                               # resumed after a preemption: already sampled
-                    j.pending = j.out[-1]
-                    self.running.append(j)
-                else:
-                    self._take(j, j.sample(row))
-            return
-        if not self.running:
-            if self.waiting:
-                raise RuntimeError("KV cache too small for the next request")
-            return
+        # decode every running job; where a domain's pages for this step are short, preempt its youngest jobs
         oldest = min(self.running, key=lambda j: j.admit)           # always keeps making progress
-        for h in range(world):
+        for h in range(doms):
             while True:
-                mine = [j for j in self.running if j.req.home == h]
-                need = sum(eng.pages_for(j.req, j.req.seq_len + 1) for j in mine)
-                if need <= eng.pages_available(h):
+                need = sum(eng.pages_for(j.req, j.req.seq_len + 1) for j in self.running if dom(j.req) == h)
+                if need <= avail(h):
                     break
-                victims = sorted((j for j in mine if j is not oldest), key=lambda j: -j.admit)
+                victims = sorted((j for j in self.running + self.prefilling if dom(j.req) == h and j is not oldest),
+                                 key=lambda j: -j.admit)
                 if not victims:
-                    raise RuntimeError(f"KV cache of rank {h} too small for its running request")
+                    raise RuntimeError("KV cache too small for the running request")
                 self._retract(victims[0])
         self.steps["decode"] += 1
         run, self.running = self.running, []

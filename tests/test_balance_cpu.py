@@ -151,14 +151,26 @@ def _owner_worker(rank, world, port, q):
         mine = sum(len(r.pages) for r in reqs)
         for r in reqs:
             e.release(r)
-        q.put((rank, outs, hist, homes, mine, used, e.cache.alloc.num_free()))
+        # chunked prefill (per-row attention over each home rank's cached chunks), then the same decode steps
+        reqs = [e.add_request(p) for p in _prompts(cfg)]
+        logits = e.prefill_chunked(reqs, 24)
+        hist2 = [logits.tolist()]
+        nxt = torch.argmax(logits, -1).tolist()
+        for _ in range(4):
+            logits = e.decode(reqs, nxt)
+            hist2.append(logits.tolist())
+            nxt = torch.argmax(logits, -1).tolist()
+        for r in reqs:
+            e.release(r)
+        q.put((rank, outs, hist, homes, mine, used, e.cache.alloc.num_free(), hist2))
     finally:
         dist.destroy_process_group()
 
 
 def test_dp_owner_kv_matches_single_rank_and_splits_pages():
     """Owner-only KV (2 DP ranks): each request's KV lives on its home rank only, yet the served tokens and logits
-    equal the single-rank engine's; the ranks' page counts add up to the single rank's."""
+    equal the single-rank engine's, with whole-prompt and with chunked prefill; the ranks' page counts add up to the
+    single rank's."""
     import torch.multiprocessing as mp
 
     from carbon_b200.engine.engine import Engine
@@ -183,9 +195,11 @@ def test_dp_owner_kv_matches_single_rank_and_splits_pages():
         p.join(timeout=60)
         assert p.exitcode == 0
     total_pages = 0
-    for rank, outs, hist, homes, mine, used, free_after in res:
+    for rank, outs, hist, homes, mine, used, free_after, hist2 in res:
         assert outs == ref_out, (rank, outs, ref_out)
         for a, b in zip(hist, ref_hist):
+            assert (torch.tensor(a) - b).abs().max() < 1e-3
+        for a, b in zip(hist2, ref_hist):                             # chunked prefill: the same logits
             assert (torch.tensor(a) - b).abs().max() < 1e-3
         assert sorted(set(homes)) == [0, 1]                         # both ranks own requests
         assert used == mine                                          # pages only for this rank's own requests
@@ -195,7 +209,7 @@ def test_dp_owner_kv_matches_single_rank_and_splits_pages():
     assert total_pages == sum((n + 15) // 16 for n in lens)         # the KV of each request is held once
 
 
-def _owner_sched_worker(rank, world, port, q, num_pages):
+def _owner_sched_worker(rank, world, port, q, num_pages, prefill_tokens):
     import os
     from datetime import timedelta
 
@@ -215,7 +229,7 @@ def _owner_sched_worker(rank, world, port, q, num_pages):
         w = init_weights(cfg, seed=0)
         e = Engine(cfg, device="cpu", source=WeightSource(cfg, state=w), num_pages=num_pages, page_size=16,
                    pctx=DistCtx(rank, world, attn_dp=True), dp_owner_kv=True)
-        s = Scheduler(e, prefill_tokens=4096)
+        s = Scheduler(e, prefill_tokens=prefill_tokens)
         ids = [s.submit(p, 40) for p in _sched_prompts(cfg)]
         out = s.run()
         q.put((rank, [out[i] for i in ids], s.preemptions, e.cache.alloc.num_free()))
@@ -230,7 +244,7 @@ def _sched_prompts(cfg):
 def test_scheduler_with_dp_owner_kv_under_pressure():
     """The serving loop over 2 DP ranks with owner-only KV: homes chosen at admission, pages budgeted per rank.
     With a per-rank cache too small for its two requests' final footprint, the ranks preempt in step (same
-    decisions on both) and every request still gets the single-rank engine's tokens."""
+    decisions on both) and every request still gets the single-rank engine's tokens, also with chunked prefill."""
     import torch.multiprocessing as mp
 
     from carbon_b200.engine.engine import Engine
@@ -245,14 +259,14 @@ def test_scheduler_with_dp_owner_kv_under_pressure():
     ids = [s.submit(p, 40) for p in _sched_prompts(cfg)]
     out = s.run()
     ref = [out[i] for i in ids]
-    for num_pages, pressured in ((64, False), (9, True)):
+    for num_pages, pressured, chunk in ((64, False, 4096), (9, True, 4096), (9, True, 20)):
         sk = socket.socket()
         sk.bind(("127.0.0.1", 0))
         port = sk.getsockname()[1]
         sk.close()
         ctx = mp.get_context("spawn")
         q = ctx.Queue()
-        ps = [ctx.Process(target=_owner_sched_worker, args=(r, 2, port, q, num_pages)) for r in range(2)]
+        ps = [ctx.Process(target=_owner_sched_worker, args=(r, 2, port, q, num_pages, chunk)) for r in range(2)]
         for p in ps:
             p.start()
         res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda x: x[0])
