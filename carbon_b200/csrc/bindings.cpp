@@ -72,6 +72,7 @@ void rms_norm(torch::Tensor x, torch::Tensor w, c10::optional<torch::Tensor> y, 
   int ldy = D;
   if (y.has_value()) { CHECK_DT((*y), at::kBFloat16); TORCH_CHECK(y->stride(1) == 1); ldy = y->stride(0); }
   if (q.has_value()) { TORCH_CHECK(sf.has_value()); TORCH_CHECK(sf->numel() >= sf_words(M, D)); }
+  if (M == 0) return;                         // a rank without rows this step (empty shard): nothing to launch
   c10::cuda::CUDAGuard g(x.device());
   CK(cb::rms_norm(x.data_ptr(), x.stride(0), w.data_ptr<float>(), ptr_or_null<void>(y), ldy, ptr_or_null<void>(q),
                   ptr_or_null<uint32_t>(sf), M, D, float(eps), cur_stream()));
