@@ -340,51 +340,59 @@ class Engine:
                     out[b] = row
         return torch.stack(out)
 
+    def _row_layout(self, reqs: List[Request], rows: List[List[tuple]]):
+        """Batch layout of per-row work (prefill chunks, verify rows): ``rows[b]`` holds request b's rows as
+        (page table, keys, token, late_from).  Rows are concatenated, or, with owner-only KV, grouped by home rank
+        with each rank's block padded to the busiest rank's count (pad rows on the scratch page).  Returns the
+        flat (tables, lengths, ids, late) lists and the position of each request's first row."""
+        tables, lens, ids, late, first = [], [], [], [], [0] * len(reqs)
+        if self.dp_owner_kv:
+            world = self.model.pctx.world
+            groups = [[b for b, r in enumerate(reqs) if r.home == h] for h in range(world)]
+            width = max(sum(len(rows[b]) for b in g) for g in groups)
+        else:
+            groups, width = [list(range(len(reqs)))], 0
+        for g in groups:
+            k0 = len(ids)
+            for b in g:
+                first[b] = len(ids)
+                for tb, n, tok, lf in rows[b]:
+                    tables.append(tb)
+                    lens.append(n)
+                    ids.append(tok)
+                    late.append(lf)
+            pad = max(0, width - (len(ids) - k0))
+            tables += [[self._scratch[0]]] * pad
+            lens += [1] * pad
+            ids += [0] * pad
+            late += [0] * pad
+        return tables, lens, ids, late, first
+
     def _prefill_rows(self, reqs: List[Request], counts: List[int]) -> torch.Tensor:
         """Run the next ``counts[b]`` uncached tokens of each request as per-row attention over the paged cache
         (keys: the request's cached tokens and the rows before it).  Returns logits [B, V] of each request's last
         row of this step.  With owner-only KV the rows are grouped by home rank (requests without one get it from
         the cost-model plan) and each rank's block is padded to the busiest rank's row count."""
-        rows_pt, rows_len, ids, late, last = [], [], [], [], [0] * len(reqs)
-
-        def add_rows(b):
-            r, n = reqs[b], counts[b]
-            toks = (r.prompt + r.out)[r.n_cached:r.n_cached + n]
-            self._ensure_pages(r, r.n_cached + n)
-            table = self._table(r, r.n_cached + n)
-            for j, tok in enumerate(toks):
-                rows_pt.append(table)
-                rows_len.append(r.n_cached + j + 1)
-                ids.append(int(tok))
-                late.append(r.late_from)
-            last[b] = len(ids) - 1
-
         if self.dp_owner_kv:
-            world = self.model.pctx.world
             fresh = [b for b, r in enumerate(reqs) if r.home < 0]
-            if fresh:
+            if fresh:                               # first chunk: the cost-model plan picks the home rank
                 from ..parallel.balance import plan_prefill
 
+                world = self.model.pctx.world
                 order, bounds, _ = plan_prefill(self.cfg, [counts[b] for b in fresh], world,
                                                 [reqs[b].n_cached for b in fresh])
                 start = 0
                 for i in order:
                     reqs[fresh[i]].home = max(k for k in range(world) if bounds[k] <= start)
                     start += counts[fresh[i]]
-            groups = [[b for b, r in enumerate(reqs) if r.home == h] for h in range(world)]
-            width = max(sum(counts[b] for b in g) for g in groups)
-            for g in groups:
-                k0 = len(ids)
-                for b in g:
-                    add_rows(b)
-                pad = width - (len(ids) - k0)
-                rows_pt += [[self._scratch[0]]] * pad
-                rows_len += [1] * pad
-                ids += [0] * pad
-                late += [0] * pad
-        else:
-            for b in range(len(reqs)):
-                add_rows(b)
+        rows = []
+        for r, n in zip(reqs, counts):
+            toks = (r.prompt + r.out)[r.n_cached:r.n_cached + n]
+            self._ensure_pages(r, r.n_cached + n)
+            table = self._table(r, r.n_cached + n)
+            rows.append([(table, r.n_cached + j + 1, int(tok), r.late_from) for j, tok in enumerate(toks)])
+        rows_pt, rows_len, ids, late, first = self._row_layout(reqs, rows)
+        last = [f + n - 1 for f, n in zip(first, counts)]
         m = len(ids)
         out_loc, key_slots, n_keys, pos = decode_metadata(rows_pt, rows_len, self.page_size, m)
         dev = self.device
@@ -493,22 +501,21 @@ class Engine:
         attending to the cache plus the rows before it. Greedy acceptance keeps the longest draft prefix the target
         agrees with and adds the target's next token. Returns the accepted new tokens per request (>= 1 each).
         KV rows of rejected drafts are simply overwritten later (positions are slot-addressed)."""
-        if self.dp_owner_kv:
-            raise NotImplementedError("speculative verify with dp_owner_kv")
-        rows_pt, rows_len, ids, late = [], [], [], []
+        rows = []
         for r, t, d in zip(reqs, last_tokens, drafts):
+            if self.dp_owner_kv and not 0 <= r.home < self.model.pctx.world:
+                raise RuntimeError(f"request {r.rid} has no home rank (prefill it on this engine first)")
             base = r.seq_len
             seq = [int(t)] + [int(x) for x in d]
             self._ensure_pages(r, base + len(seq))
-            for j, tok in enumerate(seq):
-                rows_pt.append(r.pages)
-                rows_len.append(base + j + 1)
-                ids.append(tok)
-                late.append(r.late_from)
+            table = self._table(r, base + len(seq))
+            rows.append([(table, base + j + 1, tok, r.late_from) for j, tok in enumerate(seq)])
+        rows_pt, rows_len, ids, late, first = self._row_layout(reqs, rows)
         n = len(ids)
         # verify rows are decode rows (one token each, its own key list): a captured decode graph of a large enough
-        # bucket serves them (the reference captures verify buckets of 6-row multiples)
-        bucket = self._bucket(n) if self.cuda_graphs else None
+        # bucket serves them (the reference captures verify buckets of 6-row multiples).  Owner-only KV runs them
+        # eagerly: its per-rank padded blocks need the exact row count.
+        bucket = self._bucket(n) if self.cuda_graphs and not self.dp_owner_kv else None
         out_loc, key_slots, n_keys, pos = decode_metadata(rows_pt, rows_len, self.page_size, bucket or n)
         dev = self.device
         with self.metrics.step("verify", n, len(reqs)):
@@ -526,8 +533,8 @@ class Engine:
                                   late_from=torch.tensor(late, dtype=torch.int32).to(dev))
                 logits = self.model.forward(fb, self.cache)
         pred = torch.argmax(logits.float(), dim=-1).tolist()
-        accepted, i = [], 0
-        for r, t, d in zip(reqs, last_tokens, drafts):
+        accepted = []
+        for r, t, d, i in zip(reqs, last_tokens, drafts, first):
             k = len(d) + 1
             p = pred[i:i + k]
             a = 0
@@ -537,8 +544,7 @@ class Engine:
             r.out += [int(t)] + [int(x) for x in d[:a]]      # tokens whose KV is now valid in the cache
             r.n_cached = r.seq_len
             accepted.append(new)
-            i += k
-        self.stats["decode_tokens"] += n
+        self.stats["decode_tokens"] += sum(len(x) for x in rows)
         return accepted
 
     def generate_speculative(self, prompts: List[Sequence[int]], max_new_tokens: int, drafter=None, n_draft: int = 5):

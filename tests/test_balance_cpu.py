@@ -162,15 +162,16 @@ def _owner_worker(rank, world, port, q):
             nxt = torch.argmax(logits, -1).tolist()
         for r in reqs:
             e.release(r)
-        q.put((rank, outs, hist, homes, mine, used, e.cache.alloc.num_free(), hist2))
+        spec = e.generate_speculative(_prompts(cfg), 5, n_draft=3)     # verify rows grouped by home rank
+        q.put((rank, outs, hist, homes, mine, used, e.cache.alloc.num_free(), hist2, spec))
     finally:
         dist.destroy_process_group()
 
 
 def test_dp_owner_kv_matches_single_rank_and_splits_pages():
     """Owner-only KV (2 DP ranks): each request's KV lives on its home rank only, yet the served tokens and logits
-    equal the single-rank engine's, with whole-prompt and with chunked prefill; the ranks' page counts add up to the
-    single rank's."""
+    equal the single-rank engine's, with whole-prompt and chunked prefill and with speculative verify; the ranks'
+    page counts add up to the single rank's."""
     import torch.multiprocessing as mp
 
     from carbon_b200.engine.engine import Engine
@@ -195,8 +196,9 @@ def test_dp_owner_kv_matches_single_rank_and_splits_pages():
         p.join(timeout=60)
         assert p.exitcode == 0
     total_pages = 0
-    for rank, outs, hist, homes, mine, used, free_after, hist2 in res:
+    for rank, outs, hist, homes, mine, used, free_after, hist2, spec in res:
         assert outs == ref_out, (rank, outs, ref_out)
+        assert spec == ref_out, (rank, spec, ref_out)
         for a, b in zip(hist, ref_hist):
             assert (torch.tensor(a) - b).abs().max() < 1e-3
         for a, b in zip(hist2, ref_hist):                             # chunked prefill: the same logits
