@@ -365,14 +365,10 @@ cudaError_t sparse_mla(const void* q, int T, int H, const void* kv, int S, const
            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(sparse_mla_kernel<9>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         smem_bytes<9>());
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(sparse_mla_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes<8>());
+  {
+    cudaError_t e = D == 576 ? smem_optin(sparse_mla_kernel<9>, smem_bytes<9>())
+                             : smem_optin(sparse_mla_kernel<8>, smem_bytes<8>());
     if (e != cudaSuccess) return e;
-    attr = true;
   }
   Params p;
   p.idx = idx; p.K = K; p.H = H; p.n_splits = n_splits;

@@ -970,11 +970,9 @@ cudaError_t attn_prefill(const void* q, const void* kvb, const void* kpe, int T,
       !make_tmap_2d(&tkpe, kpe, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64, T, 64 * 2, 64, BN,
                     CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(attn_prefill_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+  {
+    cudaError_t e = cb::smem_optin(attn_prefill_kernel, SMEM);
     if (e != cudaSuccess) return e;
-    attr = true;
   }
   Params p;
   p.tiles = reinterpret_cast<const int4*>(tiles);
@@ -1004,12 +1002,9 @@ cudaError_t attn_prefill2(const void* q, const void* kvb, const void* kpe, int T
       !make_tmap_2d(&tkpe, kpe, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64, T, 64 * 2, 64, BN,
                     CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(fa2::attn_prefill2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         fa2::SMEM);
+  {
+    cudaError_t e = cb::smem_optin(fa2::attn_prefill2_kernel, fa2::SMEM);
     if (e != cudaSuccess) return e;
-    attr = true;
   }
   Params p;
   p.tiles = reinterpret_cast<const int4*>(tiles);
@@ -1039,12 +1034,9 @@ cudaError_t attn_prefill3(const void* q, const void* kvb, const void* kpe, int T
       !make_tmap_2d(&tkpe, kpe, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64, T, 64 * 2, 64, fa3::BN,
                     CU_TENSOR_MAP_SWIZZLE_128B))
     return cudaErrorInvalidValue;
-  static bool attr = false;
-  if (!attr) {
-    cudaError_t e = cudaFuncSetAttribute(fa3::attn_prefill3_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         fa3::SMEM);
+  {
+    cudaError_t e = cb::smem_optin(fa3::attn_prefill3_kernel, fa3::SMEM);
     if (e != cudaSuccess) return e;
-    attr = true;
   }
   Params p;
   p.tiles = reinterpret_cast<const int4*>(tiles);

@@ -6,6 +6,9 @@
 #include <cuda_fp8.h>
 #include <stdint.h>
 #include <stdio.h>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #define CB_DEVICE __device__ __forceinline__
 #define CB_HOST_DEVICE __host__ __device__ __forceinline__
@@ -119,6 +122,27 @@ CB_DEVICE uint32_t pack_fp8x4(float a, float b, float c, float d) {
 
 CB_DEVICE float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
 CB_DEVICE float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+
+// Raise a kernel's dynamic shared-memory limit to `bytes` on the CURRENT device.  cudaFuncSetAttribute acts on
+// the current device's context only, so the opt-in is tracked per (device, kernel); the table is shared by every
+// translation unit (inline function) and guarded by a mutex, so host threads driving different GPUs may call it.
+inline cudaError_t smem_optin(const void* fn, int bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, int> done;
+  std::lock_guard<std::mutex> g(mu);
+  int& have = done[std::make_pair(dev, fn)];
+  if (have >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) have = bytes;
+  return e;
+}
+template <typename F>
+inline cudaError_t smem_optin(F* fn, int bytes) {
+  return smem_optin(reinterpret_cast<const void*>(fn), bytes);
+}
 
 CB_HOST_DEVICE int ceil_div(int a, int b) { return (a + b - 1) / b; }
 CB_HOST_DEVICE int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }

@@ -82,9 +82,11 @@ static cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, con
   cfg.stream = s;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (!resident) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  {
+    cudaError_t e = cb::smem_optin(kern, smem);
     if (e != cudaSuccess) return e;
+  }
+  if (!resident) {
     int n = 0;
     cfg.gridDim = dim3((num_sms / PAIR) * PAIR);
     if (PAIR > 1 && cudaOccupancyMaxActiveClusters(&n, kern, &cfg) == cudaSuccess && n > 0)
@@ -206,11 +208,9 @@ static cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const Ge
                           int num_sms, cudaStream_t s) {
   constexpr int smem = gemm_smem_bytes<KIND, BN, ST>();
   auto kern = gemm_tc_kernel<KIND, EPI, BN, ST, ACC>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  {
+    cudaError_t e = cb::smem_optin(kern, smem);
     if (e != cudaSuccess) return e;
-    attr_set = true;
   }
   const int grid = max_tiles < num_sms ? max_tiles : num_sms;
   if (grid <= 0) return cudaSuccess;

@@ -9,9 +9,14 @@
 // Contract:
 //   * q   [T, H, 576] bf16, kv [S, 576] bf16 (the latent cache), idx [T, K] int32 slots (-1 = no key),
 //     out [T, H, 512] bf16; all device pointers, contiguous; H <= 128.
-//   * The key list is split across CTAs exactly as the allocating entry point does; the scratch must hold
-//     T * splits * H * 514 floats.  Larger problems are rejected with cudaErrorInvalidValue before any launch, and
+//   * The key list is split across CTAs exactly as the allocating entry point does (the same split count, so both
+//     produce bitwise-identical outputs); the scratch must hold T * splits * H * 514 floats, after a 256-byte status
+//     word.  Larger problems are rejected with cudaErrorInvalidValue before any launch, and
 //     cb_noalloc_last_error() says why.
+//   * A return value of 0 means the kernels were launched.  The kernel's own waits are bounded; if one runs out the
+//     kernel stops early, leaves `out` undefined and records an error code in the status word, which every call
+//     resets to 0 on its stream.  cb_noalloc_status() copies that word back (it synchronises the stream): 0 means
+//     the last call on this device completed normally.
 //   * No cudaMalloc, cudaFree or allocating library routine is called.
 //   * The first call on a device resolves the device address of the scratch array (cudaGetSymbolAddress) with that
 //     device current; make that first call before any stream capture on that device.
@@ -27,6 +32,10 @@ extern "C" {
 // Returns a cudaError_t value (0 = success).
 int cb_sparse_mla_noalloc(const void* q, int T, int H, const void* kv, int S, const int* idx, int K, float scale,
                           void* out, cudaStream_t stream);
+
+// Status word of the last call on the current device (0 = ok; otherwise the kernel's bounded-wait error code).
+// Synchronises `stream`.  Returns a cudaError_t value.
+int cb_noalloc_status(cudaStream_t stream, int* kernel_status);
 
 // Bytes of the static scratch array, and the message of the last rejected or failed call on this thread.
 size_t cb_noalloc_scratch_bytes(void);

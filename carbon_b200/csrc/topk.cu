@@ -176,8 +176,7 @@ cudaError_t indexer_decode_logits(const void* q, const float* w, const void* kc,
   if (D != 128) return cudaErrorInvalidValue;
   const size_t smem = size_t(H) * D * 4 + H * 4;
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(indexer_decode_logits_kernel<128>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+    cudaError_t e = smem_optin(indexer_decode_logits_kernel<128>, int(smem));
     if (e != cudaSuccess) return e;
   }
   dim3 grid(T, (Lmax + 127) / 128);
@@ -255,8 +254,7 @@ cudaError_t topk_index(const float* logits, const int* key_slots, const int* n_k
   const size_t smem = size_t(Lmax) * 4;
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
   if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(topk_index_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         int(200 * 1024));
+    cudaError_t e = smem_optin(topk_index_kernel, int(200 * 1024));
     if (e != cudaSuccess) return e;
   }
   topk_index_kernel<<<T, 512, smem, s>>>(logits, key_slots, n_keys, Lmax, k, out);
@@ -268,11 +266,9 @@ cudaError_t topk_mask(const float* logits, int ldo, int Tq, int k, uint32_t* mas
   if (Tq <= 0) return cudaSuccess;
   const size_t smem = size_t(Tq) * 4;
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
-  static size_t attr = 0;
-  if (smem > 48 * 1024 && smem > attr) {
-    cudaError_t e = cudaFuncSetAttribute(topk_mask_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(200 * 1024));
+  if (smem > 48 * 1024) {
+    cudaError_t e = smem_optin(topk_mask_kernel, int(200 * 1024));
     if (e != cudaSuccess) return e;
-    attr = 200 * 1024;
   }
   topk_mask_kernel<<<Tq, 512, smem, s>>>(logits, ldo, Tq, k, mask, mask_words, row0);
   return cudaGetLastError();

@@ -68,7 +68,7 @@ def _worker(rank, world, port, q):
         table = (torch.randn(V, D, device=dev, generator=gall) * 0.02).to(torch.bfloat16)
         per = V // world
         ids = torch.randint(0, V, (230,), device=dev, generator=gall, dtype=torch.int32)
-        cfg = types.SimpleNamespace(vocab_size=V, hidden_size=D, hc_mult=4)
+        cfg = small_gpu_config().replace(vocab_size=V, hidden_size=D, hc_mult=4)
         md = types.SimpleNamespace(cfg=cfg, embed=table[rank * per:(rank + 1) * per].contiguous(), v_lo=rank * per,
                                    v_hi=(rank + 1) * per, on_gpu=True)
         mf = types.SimpleNamespace(cfg=cfg, embed=md.embed.clone(), v_lo=md.v_lo, v_hi=md.v_hi, on_gpu=True)
