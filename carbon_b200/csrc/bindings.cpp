@@ -371,16 +371,26 @@ void engram_gate(torch::Tensor X, torch::Tensor kv, torch::Tensor qw, torch::Ten
 }
 
 // decode-side DSA: q [T, H, 128] bf16, w [T, H] fp32, kc [S, 128] bf16, key_slots [T, L], n_keys [T] -> out [T, k]
+void indexer_decode_logits(torch::Tensor q, torch::Tensor w, torch::Tensor kc, torch::Tensor key_slots,
+                           torch::Tensor n_keys, torch::Tensor logits) {
+  CHECK_CUDA(q); CHECK_CONTIG(q); CHECK_CONTIG(kc); CHECK_CONTIG(key_slots); CHECK_CONTIG(logits);
+  CHECK_DT(q, at::kBFloat16); CHECK_DT(kc, at::kBFloat16); CHECK_DT(w, at::kFloat); CHECK_DT(logits, at::kFloat);
+  CHECK_DT(key_slots, at::kInt); CHECK_DT(n_keys, at::kInt);
+  const int T = q.size(0), L = key_slots.size(1);
+  TORCH_CHECK(logits.size(0) == T && logits.size(1) == L && kc.size(1) == q.size(2));
+  c10::cuda::CUDAGuard g(q.device());
+  CK(cb::indexer_decode_logits(q.data_ptr(), w.contiguous().data_ptr<float>(), kc.data_ptr(), kc.size(0),
+                               key_slots.data_ptr<int>(), n_keys.data_ptr<int>(), T, L, q.size(1), q.size(2),
+                               logits.data_ptr<float>(), nullptr, cur_stream()));
+}
+
 void indexer_topk(torch::Tensor q, torch::Tensor w, torch::Tensor kc, torch::Tensor key_slots, torch::Tensor n_keys,
                   torch::Tensor out) {
-  CHECK_CUDA(q); CHECK_CONTIG(q); CHECK_CONTIG(kc); CHECK_CONTIG(key_slots); CHECK_CONTIG(out);
-  CHECK_DT(q, at::kBFloat16); CHECK_DT(kc, at::kBFloat16); CHECK_DT(w, at::kFloat);
+  CHECK_CUDA(q); CHECK_CONTIG(out); CHECK_DT(out, at::kInt);
   const int T = q.size(0), L = key_slots.size(1);
   auto logits = torch::empty({T, L}, q.options().dtype(at::kFloat));
+  indexer_decode_logits(q, w, kc, key_slots, n_keys, logits);
   c10::cuda::CUDAGuard g(q.device());
-  CK(cb::indexer_decode_logits(q.data_ptr(), w.contiguous().data_ptr<float>(), kc.data_ptr(),
-                               key_slots.data_ptr<int>(), n_keys.data_ptr<int>(), T, L, q.size(1), q.size(2),
-                               logits.data_ptr<float>(), cur_stream()));
   CK(cb::topk_index(logits.data_ptr<float>(), key_slots.data_ptr<int>(), n_keys.data_ptr<int>(), T, L, out.size(1),
                     out.data_ptr<int>(), cur_stream()));
 }
@@ -420,4 +430,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("engram_gather", &engram_gather);
   m.def("engram_gate", &engram_gate);
   m.def("indexer_topk", &indexer_topk);
+  m.def("indexer_decode_logits", &indexer_decode_logits);
 }

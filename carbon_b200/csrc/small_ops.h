@@ -74,8 +74,10 @@ cudaError_t indexer_logits_fp8(const void* keys, const uint32_t* keys_sf, int L,
                                int num_sms, cudaStream_t s);
 cudaError_t topk_mask(const float* logits, int ldo, int Tq, int k, uint32_t* mask, int mask_words, int row0,
                       cudaStream_t s);
-cudaError_t indexer_decode_logits(const void* q, const float* w, const void* kc, const int* key_slots,
-                                  const int* n_keys, int T, int Lmax, int H, int D, float* out, cudaStream_t s);
+// tcgen05 decode indexer (indexer_decode.cu): q [T,H,128] bf16, w [T,H], indexer-key cache kc [S,128] bf16
+cudaError_t indexer_decode_logits(const void* q, const float* w, const void* kc, int S, const int* key_slots,
+                                  const int* n_keys, int T, int Lmax, int H, int D, float* out, int* status,
+                                  cudaStream_t s);
 cudaError_t topk_index(const float* logits, const int* key_slots, const int* n_keys, int T, int Lmax, int k,
                        int* out, cudaStream_t s);
 

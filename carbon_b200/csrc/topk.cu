@@ -125,67 +125,8 @@ __global__ void topk_mask_kernel(const float* __restrict__ logits, int ldo, int 
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// Decode-side DSA indexer: logits of one query token over its own key list (cache slots), then top-k slot indices.
+// Decode-side DSA top-k (the logits come from the tcgen05 kernel in indexer_decode.cu).
 // ---------------------------------------------------------------------------------------------------------------
-// grid (T, ceil(Lmax / 128)), 128 threads: thread = one key. q [T, H, D] bf16, w [T, H] fp32, kc [S, D] bf16.
-template <int D>
-__global__ void indexer_decode_logits_kernel(const __nv_bfloat16* __restrict__ q, const float* __restrict__ w,
-                                             const __nv_bfloat16* __restrict__ kc, const int* __restrict__ key_slots,
-                                             const int* __restrict__ n_keys, int Lmax, int H,
-                                             float* __restrict__ out) {
-  extern __shared__ float sq[];          // [H][D] fp32, then w[H]
-  float* sw = sq + H * D;
-  const int t = blockIdx.x;
-  for (int i = threadIdx.x; i < H * D; i += blockDim.x) sq[i] = __bfloat162float(q[size_t(t) * H * D + i]);
-  for (int i = threadIdx.x; i < H; i += blockDim.x) sw[i] = w[size_t(t) * H + i];
-  __syncthreads();
-  const int j = blockIdx.y * blockDim.x + threadIdx.x;
-  if (j >= Lmax) return;
-  const int n = n_keys[t];
-  float* o = out + size_t(t) * Lmax + j;
-  if (j >= n) { *o = -INFINITY; return; }
-  const int slot = key_slots[size_t(t) * Lmax + j];
-  if (slot < 0) { *o = -INFINITY; return; }
-  float kv[D];
-  const uint4* kr = reinterpret_cast<const uint4*>(kc + size_t(slot) * D);
-#pragma unroll
-  for (int c = 0; c < D / 8; ++c) {
-    const uint4 r = kr[c];
-    kv[8 * c + 0] = bf16_lo(r.x); kv[8 * c + 1] = bf16_hi(r.x); kv[8 * c + 2] = bf16_lo(r.y);
-    kv[8 * c + 3] = bf16_hi(r.y); kv[8 * c + 4] = bf16_lo(r.z); kv[8 * c + 5] = bf16_hi(r.z);
-    kv[8 * c + 6] = bf16_lo(r.w); kv[8 * c + 7] = bf16_hi(r.w);
-  }
-  float acc = 0.f;
-  for (int h = 0; h < H; ++h) {
-    const float4* qh = reinterpret_cast<const float4*>(sq + h * D);
-    float d0 = 0.f, d1 = 0.f;
-#pragma unroll
-    for (int c = 0; c < D / 4; c += 2) {
-      const float4 a = qh[c], b = qh[c + 1];
-      d0 += a.x * kv[4 * c] + a.y * kv[4 * c + 1] + a.z * kv[4 * c + 2] + a.w * kv[4 * c + 3];
-      d1 += b.x * kv[4 * c + 4] + b.y * kv[4 * c + 5] + b.z * kv[4 * c + 6] + b.w * kv[4 * c + 7];
-    }
-    acc += sw[h] * fmaxf(d0 + d1, 0.f);
-  }
-  *o = acc;
-}
-
-cudaError_t indexer_decode_logits(const void* q, const float* w, const void* kc, const int* key_slots,
-                                  const int* n_keys, int T, int Lmax, int H, int D, float* out, cudaStream_t s) {
-  if (T == 0) return cudaSuccess;
-  if (D != 128) return cudaErrorInvalidValue;
-  const size_t smem = size_t(H) * D * 4 + H * 4;
-  if (smem > 48 * 1024) {
-    cudaError_t e = smem_optin(indexer_decode_logits_kernel<128>, int(smem));
-    if (e != cudaSuccess) return e;
-  }
-  dim3 grid(T, (Lmax + 127) / 128);
-  indexer_decode_logits_kernel<128><<<grid, 128, smem, s>>>(reinterpret_cast<const __nv_bfloat16*>(q), w,
-                                                            reinterpret_cast<const __nv_bfloat16*>(kc), key_slots,
-                                                            n_keys, Lmax, H, out);
-  return cudaGetLastError();
-}
-
 // Top-k slot indices of each row (keys in key order, -1 padded): logits [T, Lmax], key_slots [T, Lmax].
 // Same radix select and lower-index tie rule as topk_mask_kernel; invalid keys carry -inf logits.
 __global__ void topk_index_kernel(const float* __restrict__ logits, const int* __restrict__ key_slots,

@@ -406,3 +406,26 @@ def test_indexer_topk_decode(T, L, k):
     ref = indexer_topk(q, w, kc, slots, n, k)
     for i in range(T):
         assert set(got[i][got[i] >= 0].tolist()) == set(ref[i][ref[i] >= 0].tolist()), i
+
+
+@pytest.mark.parametrize("T,L,H", [(3, 700, 64), (2, 129, 16), (5, 4100, 32), (1, 300, 128)])
+def test_indexer_decode_logits_tcgen05(T, L, H):
+    """tcgen05 decode indexer: Σ_h w·relu(q·k) over gathered key rows vs fp32; -inf past n_keys and at slot -1."""
+    torch.manual_seed(3)
+    S = 9000
+    q = torch.randn(T, H, 128).to(torch.bfloat16)
+    w = torch.randn(T, H) * 0.1
+    kc = torch.randn(S, 128).to(torch.bfloat16)
+    slots = torch.stack([torch.randperm(S)[:L] for _ in range(T)]).int()
+    n = torch.tensor([max(1, L - 131 * i) for i in range(T)], dtype=torch.int32)
+    slots[:, 5] = -1                                        # a hole inside the valid range
+    out = torch.empty(T, L, device=DEV)
+    _ext().indexer_decode_logits(q.to(DEV), w.to(DEV), kc.to(DEV), slots.to(DEV), n.to(DEV), out)
+    out = out.cpu()
+    for t in range(T):
+        nt = int(n[t])
+        s = slots[t, :nt].clamp(min=0).long()
+        ref = ((q[t].float() @ kc[s].float().t()).clamp(min=0) * w[t][:, None]).sum(0)
+        valid = slots[t, :nt] >= 0
+        assert torch.isinf(out[t, :nt][~valid]).all() and torch.isinf(out[t, nt:]).all()
+        assert rel_err(out[t, :nt][valid], ref[valid]) < 1e-5, t
