@@ -6,6 +6,7 @@ measured roofline (``MEASURED_PEAKS.json`` when present: ``bf16_tflops``, ``hbm_
     python -m carbon_b200.benchmarks gemm  [--m 16384 --n 24576 --k 7168]             # fp8 block-scaled GEMM
     python -m carbon_b200.benchmarks moe   [--tokens 4096 --experts 256 --topk 8]     # config 4, one GPU
     python -m carbon_b200.benchmarks decode_attn [--batch 32 --topk 2048]
+    python -m carbon_b200.benchmarks decode_indexer [--batch 32 --context 4096 --topk 2048]
 
 Each prints one JSON line.  Inputs are larger than L2 where the config allows; between timed iterations a 256 MB
 buffer is rewritten to flush L2 (``flush_l2``) for the ones that are not.
@@ -161,6 +162,34 @@ def bench_decode_attn(a):
                       "tflops": round(T * H * K * (576 + 512) * 2 / ms / 1e9, 1), "peak_src": pk["src"]}))
 
 
+def bench_decode_indexer(a):
+    """Decode DSA indexer: logits of `batch` tokens over `context` paged keys each (64-token pages), then top-k."""
+    from .ops._ext import ext
+
+    T, L, H, k = a.batch, a.context + 1, 64, a.topk
+    page = 64
+    S = T * (L // page + 2) * page
+    q = torch.randn(T, H, 128, device="cuda").to(torch.bfloat16)
+    w = torch.randn(T, H, device="cuda") * 0.01
+    kc = torch.randn(S, 128, device="cuda").to(torch.bfloat16)
+    perm = torch.randperm(S // page, device="cuda")
+    pages = perm[: T * (L // page + 1)].view(T, -1)
+    pos = torch.arange(L, device="cuda")
+    slots = (pages[:, pos // page] * page + pos % page).int().contiguous()
+    n = torch.full((T,), L, dtype=torch.int32, device="cuda")
+    logits = torch.empty(T, L, device="cuda")
+    out = torch.empty(T, k, dtype=torch.int32, device="cuda")
+    e = ext()
+    ms_logits = time_fn(lambda: e.indexer_decode_logits(q, w, kc, slots, n, logits))
+    ms_all = time_fn(lambda: e.indexer_topk(q, w, kc, slots, n, out))
+    bytes_k = T * L * 128 * 2
+    pk = peaks()
+    print(json.dumps({"bench": "indexer_decode", "batch": T, "keys": L, "heads": H, "topk": k,
+                      "logits_us": round(ms_logits * 1e3, 2), "logits_plus_topk_us": round(ms_all * 1e3, 2),
+                      "logits_frac_of_hbm": round(bytes_k / ms_logits / 1e6 / pk["hbm_gbs"], 3),
+                      "peak_src": pk["src"]}))
+
+
 def bench_moe(a):
     """Config 4 MoE layer (router top-k + routed experts + shared expert) on one GPU, or EP over all ranks of a
     torchrun job (``--comm fused|nccl``): 256 experts top-8 + 1 shared, hidden 7168, intermediate 2048, fp8
@@ -226,7 +255,7 @@ def bench_moe(a):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["attn", "gemm", "mhc", "decode_attn", "moe"])
+    ap.add_argument("what", choices=["attn", "gemm", "mhc", "decode_attn", "decode_indexer", "moe"])
     ap.add_argument("--experts", type=int, default=256)
     ap.add_argument("--inter", type=int, default=2048)
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"])
@@ -249,7 +278,7 @@ def main(argv=None):
     a = ap.parse_args(argv)
     sys.path.insert(0, ROOT)
     {"attn": bench_attn, "gemm": bench_gemm, "mhc": bench_mhc, "decode_attn": bench_decode_attn,
-     "moe": bench_moe}[a.what](a)
+     "decode_indexer": bench_decode_indexer, "moe": bench_moe}[a.what](a)
 
 
 if __name__ == "__main__":

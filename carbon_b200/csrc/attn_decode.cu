@@ -3,14 +3,16 @@
 //   o_lat[t, h, :] = softmax_j( q[t, h, :] · kv[idx[t, j], :] · scale ) · kv[idx[t, j], :512]
 //
 // q: [T, H, 576] bf16 (512 absorbed-nope + 64 rope), kv: latent cache [S, 576] bf16, idx: [T, K] int32 cache slots
-// (-1 = no key).  All H <= 128 heads of a token share every KV row (MQA), so a CTA computes S[128 heads, 16 keys]
+// (-1 = no key).  All H <= 128 heads of a token share every KV row (MQA), so a CTA computes S[128 heads, 32 keys]
 // = Q·Kᵀ with M = 128 (heads) and streams the token's selected rows through shared memory with TMA gather4 (four
 // 128-byte row pieces per instruction, one-row-high box).  The value half (256 of the 512 latent dims) of the CTA
-// accumulates O[128, 256] in TMEM; the other half is computed by a sibling CTA (both need all of S).  Keys are split
-// across CTAs (flash-decoding); a combine kernel merges the (m, l, O) partials.
+// accumulates O[128, 256] in TMEM; the other half is computed by a sibling CTA (both need all of S).  S is
+// double-buffered in TMEM and the softmax writes P back over its S buffer as bf16, where the P·V MMA reads it as
+// its A operand (no shared-memory round trip for P).  Keys are split across CTAs (flash-decoding); a combine kernel
+// merges the (m, l, O) partials.
 //
-// Roles (256 threads): warp 0 TMA (Q once, then gathered KV tiles, 3-stage ring), warp 1 MMA, warp 2 TMEM,
-// warps 4-7 softmax (one head row per thread, lazy O rescale).  Every wait is bounded.
+// Roles (256 threads): warp 0 TMA (Q once, then gathered KV tiles, 2-stage ring of 32-key tiles), warp 1 MMA,
+// warp 2 TMEM, warps 4-7 softmax (one head row per thread, lazy O rescale).  Every wait is bounded.
 // Reference kernels with the same role: FlashMLA-derived decode / verify attention over the paged latent cache
 // (king_v10/bundle_v9/dec/cuda_decode_attn.py:20-116, dec/cuda_vattn.py:4654).
 #include <cudaTypedefs.h>
@@ -23,16 +25,15 @@ constexpr int HM = 128;                // head rows per CTA (M)
 // A row is NA 64-dim atoms: NA = 9 for MLA (512 latent + 64 RoPE key), NA = 8 for latent MQA (one 512-dim head whose
 // last 64 dims carry RoPE).  The value is always the first DL = 512 dims of the row.
 constexpr int D = 576, DL = 512, DHALF = 256;
-constexpr int KT = 16;                 // keys per tile (N of Q·Kᵀ, K of P·V)
-constexpr int STAGES = 3;
+constexpr int KT = 32;                 // keys per tile (N of Q·Kᵀ, K of P·V)
+constexpr int STAGES = 2;
 constexpr int Q_ATOM = HM * 128;       // 16 KB: 128 rows x 64 dims
-constexpr int KV_ATOM = KT * 128;      // 2 KB: 16 rows x 64 dims
-constexpr int Q_BYTES = 9 * Q_ATOM;    // 144 KB
-constexpr int KV_BYTES = 9 * KV_ATOM;  // 18 KB per stage
-constexpr int P_BYTES = HM * 128;      // 16 KB (16 keys used of a 64-key swizzle atom)
-constexpr int SMEM = 1024 + Q_BYTES + STAGES * KV_BYTES + P_BYTES + 256;
+constexpr int KV_ATOM = KT * 128;      // 4 KB: 32 rows x 64 dims
+// TMEM: O [128 x 256] fp32 at columns [0, 256); two S buffers of 64 columns at 256 and 320 (P overwrites the first
+// KT/2 columns of its S buffer as packed bf16 and is read there by the P·V MMA)
+constexpr int TM_O = 0, TM_S = 256, TM_S_STRIDE = 64;
 template <int NA>
-constexpr int smem_bytes() { return 1024 + NA * Q_ATOM + STAGES * NA * KV_ATOM + P_BYTES + 256; }
+constexpr int smem_bytes() { return 1024 + NA * Q_ATOM + STAGES * NA * KV_ATOM + 256; }
 constexpr float kRescaleThresh = 8.0f;
 
 struct Params {
@@ -63,6 +64,12 @@ CB_DEVICE void tma_gather4(void* dst, const void* tmap, uint64_t* bar, int col, 
       : "memory");
 }
 
+// Pipeline (one CTA = one token, one value half, one key split):
+//   TMA   Q once; KV tile j into stage j % 2 after P·V(j-2) released it
+//   MMA   QK(0) QK(1) | PV(0) QK(2) | PV(1) QK(3) | ...   S(j) goes to buffer j % 2; PV(j) reads P(j) from the same
+//         columns and QK(j+2) overwrites them afterwards (tcgen05 MMAs of one thread execute in issue order)
+//   softmax (one head row per thread) of tile j+1 runs while PV(j) and QK(j+2) are on the tensor pipe; O is
+//         rescaled lazily, only when the running max grows by more than 2^8, after waiting for the previous PV.
 template <int NA>
 __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constant__ CUtensorMap tm_q,
                                                             const __grid_constant__ CUtensorMap tm_kv,
@@ -73,16 +80,14 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sKV = sQ + Q_BYTES;
-  uint8_t* sP = sKV + STAGES * KV_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + P_BYTES);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + STAGES * KV_BYTES);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;              // [STAGES]
-  uint64_t* kv_empty = bars + 1 + STAGES;    // [STAGES]
-  uint64_t* s_full = bars + 1 + 2 * STAGES;  // [2]
-  uint64_t* s_empty = s_full + 2;            // [2]
-  uint64_t* p_full = s_empty + 2;
-  uint64_t* pv_done = p_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 1);
+  uint64_t* kv_empty = kv_full + STAGES;     // [STAGES]
+  uint64_t* s_full = kv_empty + STAGES;      // [2]
+  uint64_t* p_full = s_full + 2;             // [2]
+  uint64_t* pv_done = p_full + 2;            // [2]: PV(j) completes phase j >> 1 of pv_done[j & 1]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int t = blockIdx.x, hh = blockIdx.y, split = blockIdx.z;
@@ -95,8 +100,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < STAGES; ++i) { mbar_init(&kv_full[i], 1); mbar_init(&kv_empty[i], 1); }
-    for (int i = 0; i < 2; ++i) { mbar_init(&s_full[i], 1); mbar_init(&s_empty[i], 128); }
-    mbar_init(p_full, 128); mbar_init(pv_done, 1);
+    for (int i = 0; i < 2; ++i) { mbar_init(&s_full[i], 1); mbar_init(&p_full[i], 128); mbar_init(&pv_done[i], 1); }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -116,8 +120,8 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
     }
     for (int j = 0; j < n_tiles; ++j) {
       const int s = j % STAGES;
-      const int key = k_begin + j * KT + lane;
-      int slot = (lane < KT && key < k_end) ? idx_t[key] : 0;
+      const int key = k_begin + j * KT + lane;                 // KT == 32: one key per lane
+      int slot = key < k_end ? __ldg(idx_t + key) : 0;
       if (slot < 0) slot = 0;                                  // masked in softmax; keep the address valid
       int ok = 1;
       if (lane == 0) {
@@ -130,10 +134,10 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
       int r[KT];
 #pragma unroll
       for (int i = 0; i < KT; ++i) r[i] = __shfl_sync(0xffffffffu, slot, i);
-      if (lane < NA) {                                         // lane a issues the 4 gathers of 64-dim atom a
+      if (lane < NA) {                                         // lane a issues the 8 gathers of 64-dim atom a
         uint8_t* dst = sKV + s * KV_BYTES + lane * KV_ATOM;
 #pragma unroll
-        for (int g = 0; g < 4; ++g)
+        for (int g = 0; g < KT / 4; ++g)
           tma_gather4(dst + g * 4 * 128, &tm_kv, &kv_full[s], lane * 64, r[4 * g], r[4 * g + 1], r[4 * g + 2],
                       r[4 * g + 3]);
       }
@@ -141,38 +145,42 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
     }
   } else if (warp == 1) {
     // ---------------- MMA ----------------
-    if (elect_one()) {
+    if (elect_one() && n_tiles > 0) {
       const uint32_t id_qk = idesc_bf16(HM, KT);
       const uint32_t id_pv = idesc_bf16(HM, DHALF) | (1u << 16);   // B (V) MN-major
-      bool ok = n_tiles == 0 || mbar_wait(q_full, 0);
+      bool ok = mbar_wait(q_full, 0);
       if (!ok) fail(kErrTimeoutFull);
       auto issue_qk = [&](int j) -> bool {
         const int s = j % STAGES, b = j & 1;
         if (!mbar_wait(&kv_full[s], (j / STAGES) & 1)) { fail(kErrTimeoutFull); return false; }
-        if (!mbar_wait(&s_empty[b], ((j >> 1) & 1) ^ 1)) { fail(kErrTimeoutTmem); return false; }
         tc_fence_after();
+#pragma unroll 4
         for (int kk = 0; kk < D / 16; ++kk) {
           const int a = kk >> 2, off = (kk & 3) * 32;
-          mma_f16_ss(tmem + b * 32, smem_desc_sw128(sQ + a * Q_ATOM + off),
+          mma_f16_ss(tmem + TM_S + b * TM_S_STRIDE, smem_desc_sw128(sQ + a * Q_ATOM + off),
                      smem_desc_sw128(sKV + s * KV_BYTES + a * KV_ATOM + off), id_qk, kk > 0);
         }
         mma_commit(&s_full[b]);
         return true;
       };
       auto issue_pv = [&](int j) -> bool {
-        const int s = j % STAGES;
-        if (!mbar_wait(p_full, j & 1)) { fail(kErrTimeoutFull); return false; }
+        const int s = j % STAGES, b = j & 1;
+        if (!mbar_wait(&p_full[b], (j >> 1) & 1)) { fail(kErrTimeoutFull); return false; }
         tc_fence_after();
-        mma_f16_ss(tmem + 256, smem_desc_sw128(sP),
-                   desc_mn_sw128(sKV + s * KV_BYTES + (hh * 4) * KV_ATOM, KV_ATOM, 1024), id_pv, j > 0);
-        mma_commit(pv_done);
+#pragma unroll
+        for (int k = 0; k < KT / 16; ++k)
+          mma_f16_ts(tmem + TM_O, tmem + TM_S + b * TM_S_STRIDE + 8 * k,
+                     desc_mn_sw128(sKV + s * KV_BYTES + (hh * 4) * KV_ATOM + k * 16 * 128, KV_ATOM, 1024), id_pv,
+                     (j > 0 || k > 0) ? 1u : 0u);
+        mma_commit(&pv_done[b]);
         mma_commit(&kv_empty[s]);
         return true;
       };
-      if (ok && n_tiles > 0) ok = issue_qk(0);
+      if (ok) ok = issue_qk(0);
+      if (ok && n_tiles > 1) ok = issue_qk(1);
       for (int j = 0; ok && j < n_tiles && !*abort_flag; ++j) {
-        if (j + 1 < n_tiles) ok = issue_qk(j + 1);
-        if (ok) ok = issue_pv(j);
+        ok = issue_pv(j);
+        if (ok && j + 2 < n_tiles) ok = issue_qk(j + 2);
       }
     }
   } else if (warp >= 4) {
@@ -186,18 +194,17 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
       const int b = j & 1;
       if (!mbar_wait(&s_full[b], (j >> 1) & 1)) { fail(kErrTimeoutTmem); ok = false; break; }
       tc_fence_after();
-      uint32_t r[16];
-      tmem_ld_32x32b_x16(t_lane + b * 32, r);
+      uint32_t r[KT];
+      tmem_ld_32x32b_x32(t_lane + TM_S + b * TM_S_STRIDE, r);
+      // validity of the tile's keys (one per lane), as a bit mask shared by the warp
+      const int my_key = k_begin + j * KT + lane;
+      const uint32_t vmask = __ballot_sync(0xffffffffu, my_key < k_end && __ldg(idx_t + my_key) >= 0);
       tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(&s_empty[b]);
       float sv[KT];
       float mt = -INFINITY;
 #pragma unroll
       for (int i = 0; i < KT; ++i) {
-        const int key = k_begin + j * KT + i;
-        const bool valid = key < k_end && __ldg(idx_t + key) >= 0;
-        sv[i] = valid ? __uint_as_float(r[i]) * p.scale_log2 : -INFINITY;
+        sv[i] = ((vmask >> i) & 1u) ? __uint_as_float(r[i]) * p.scale_log2 : -INFINITY;
         mt = fmaxf(mt, sv[i]);
       }
       const bool need = (j > 0) && (mt > m_used + kRescaleThresh);
@@ -205,42 +212,38 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
       const float m_ref = m_new == -INFINITY ? 0.f : m_new;
       float alpha = 1.f;
       if (need && m_used != -INFINITY) alpha = exp2f(m_used - m_ref);
-      float rs = 0.f;
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // O holds the sums of earlier tiles at the old max: wait for the last PV, then rescale it in TMEM
+        if (!mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1)) { fail(kErrTimeoutTmem); ok = false; break; }
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < DHALF; c += 32) {
+          uint32_t o[32];
+          tmem_ld_32x32b_x32(t_lane + TM_O + c, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st_32x32b_x32(t_lane + TM_O + c, o);
+        }
+      }
+      float rs0 = 0.f, rs1 = 0.f;
       uint32_t pk[KT / 2];
 #pragma unroll
       for (int i = 0; i < KT; i += 2) {
         const float a0 = exp2f(sv[i] - m_ref), a1 = exp2f(sv[i + 1] - m_ref);
-        rs += a0 + a1;
+        rs0 += a0;
+        rs1 += a1;
         pk[i / 2] = pack_bf16x2(a0, a1);
       }
-      l = l * alpha + rs;
+      tmem_st_32x32b_x16(t_lane + TM_S + b * TM_S_STRIDE, pk);   // P over the first KT/2 columns of S(j)
+      l = l * alpha + (rs0 + rs1);
       m_used = m_new;
-      if (j > 0) {
-        if (!mbar_wait(pv_done, (j - 1) & 1)) { fail(kErrTimeoutTmem); ok = false; break; }
-        tc_fence_after();
-        if (__any_sync(0xffffffffu, need)) {
-#pragma unroll 1
-          for (int c = 0; c < DHALF; c += 16) {
-            uint32_t o[16];
-            tmem_ld_32x32b_x16(t_lane + 256 + c, o);
-            tmem_ld_wait();
-#pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st_32x32b_x16(t_lane + 256 + c, o);
-          }
-          tmem_st_wait();
-        }
-      }
-      // P row: 16 keys = the first two 16-byte chunks of a 128-byte swizzled row
-      uint8_t* prow = sP + row * 128;
-      *reinterpret_cast<uint4*>(prow + ((0 ^ (row & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      *reinterpret_cast<uint4*>(prow + ((1 ^ (row & 7)) << 4)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-      fence_proxy_async();
+      tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(p_full);
+      mbar_arrive(&p_full[b]);
     }
     if (ok && n_tiles > 0) {
-      if (!mbar_wait(pv_done, (n_tiles - 1) & 1)) { fail(kErrTimeoutTmem); ok = false; }
+      if (!mbar_wait(&pv_done[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1)) { fail(kErrTimeoutTmem); ok = false; }
       tc_fence_after();
     }
     const bool head_ok = row < p.H;
@@ -262,7 +265,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
       for (int c = 0; c < DHALF; c += 32) {
         uint32_t v[32];
         if (n_tiles > 0) {
-          tmem_ld_32x32b_x32(t_lane + 256 + c, v);
+          tmem_ld_32x32b_x32(t_lane + TM_O + c, v);
           tmem_ld_wait();
         } else {
 #pragma unroll

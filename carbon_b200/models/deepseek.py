@@ -162,6 +162,8 @@ class DeepseekModel:
         if cfg.swa_window and cfg.attn_kind != "latent_mqa":
             raise NotImplementedError("swa_window is served by the latent-MQA attention path only")
         tp, ep = self.pctx.tp, self.pctx.ep
+        # TP attention whose output projection runs on each token's owner after a heads -> tokens all-to-all
+        self.o_a2a = bool(getattr(self.pctx, "oproj_a2a", False)) and tp > 1
         self.H_local = cfg.n_heads // tp
         self.E_local = cfg.n_routed_experts // ep if cfg.n_routed_experts else 0
         dev = self.device
@@ -298,20 +300,28 @@ class DeepseekModel:
             wkv_b3 = (L.wkv_b.fw.dequant() if L.wkv_b.kind == "fp8" else wkv_b).view(Hl, dn + dv, r)
             L.w_uk = wkv_b3[:, :dn, :].transpose(1, 2).contiguous().to(self.act_dtype)  # [Hl, r, dn]
             L.w_uv = wkv_b3[:, dn:, :].contiguous().to(self.act_dtype)                  # [Hl, dv, r]
+            L.w_uv_all = None
+            if self.o_a2a:
+                # every head's value up-projection: the absorbed decode output stays token-major on its owner
+                wall = get(a + "wkv_b.weight")
+                if self.on_gpu and self.fp8:
+                    wall = Lin(wall, dev, self.fp8).fw.dequant()
+                L.w_uv_all = wall.view(H, dn + dv, r)[:, dn:, :].contiguous().to(self.act_dtype)  # [H, dv, r]
+                del wall
         L.wo_a = None
         if cfg.o_groups:
             # grouped low-rank output projection: this rank's heads are whole groups
             G, R = cfg.o_groups, cfg.o_lora_rank
             if G % pc.tp:
                 raise ValueError(f"o_groups={G} must be a multiple of the attention TP degree {pc.tp}")
-            Gl = G // pc.tp
-            g0 = pc.tp_rank * Gl
+            Gl = G if self.o_a2a else G // pc.tp          # the owner of a token projects all of its groups
+            g0 = 0 if self.o_a2a else pc.tp_rank * Gl
             L.wo_a = get(a + "wo_a.weight", slice(g0, g0 + Gl)).to(self.act_dtype).contiguous()  # [Gl, R, (H/G)*dvh]
             wo_b = get(a + "wo_b.weight")                                                      # [D, G*R]
             L.wo = Lin(wo_b[:, g0 * R:(g0 + Gl) * R].contiguous(), dev, self.fp8)
         else:
             wo = get(a + "wo.weight")                                              # [D, H*dvh]
-            L.wo = Lin(wo[:, h0 * dvh:h1 * dvh].contiguous(), dev, self.fp8)
+            L.wo = Lin(wo if self.o_a2a else wo[:, h0 * dvh:h1 * dvh].contiguous(), dev, self.fp8)
         L.sink = get(a + "sink")[h0:h1].float().contiguous() if cfg.attn_sink else None
         L.sink_all = get(a + "sink").float().contiguous().to(dev) if cfg.attn_sink else None     # every head
         L.engram = None
@@ -481,13 +491,18 @@ class DeepseekModel:
             if not self.on_gpu:
                 q = q.clone()
             C.rope_(q, dq - dr, dr, self.cos_sin, pos_l if dp else fb.pos)
+        tok_major = False        # o holds this rank's tokens with every head (else: every token, this rank's heads)
         if cfg.attn_kind == "latent_mqa":
-            o = self._attn_latent(i, q, fb, cache, idx_l, dp)
+            o, tok_major = self._attn_latent(i, q, fb, cache, idx_l, dp)
         elif fb.is_prefill:
             o = self._attn_prefill(i, q, latent, fb, idx_l, cache, dp)
         else:
-            o = self._attn_decode(i, q, fb, cache, idx_l, dp)
+            o, tok_major = self._attn_decode(i, q, fb, cache, idx_l, dp)
         with region("attn.o_proj"):
+            if self.o_a2a:
+                if not tok_major:
+                    o = pc.heads_to_tokens(o.to(self.act_dtype).contiguous())          # [T_l, H, dvh]
+                return L.wo(self._out_heads(L, o, o.shape[0]))
             o2 = self._out_heads(L, o, T)
             return L.wo(o2) if dp else pc.row_parallel_out(L.wo, o2)
 
@@ -635,16 +650,18 @@ class DeepseekModel:
         rows = slice(lo, hi) if local else slice(0, q.shape[0])
         idx = self._latent_keys(i, fb, cache, idx_l, rows, local)
         pos_q = fb.pos[lo:hi] if dp else fb.pos
+        tok_major = swap and self.o_a2a      # the owner keeps its tokens' outputs (all heads) for the projection
         with region("attn.core_prefill" if fb.is_prefill else "attn.core_decode"):
             if swap:
                 q_tok = pc.heads_to_tokens(q.contiguous())                          # [n_r, H, r]
-                o_tok = A.sparse_mla(q_tok, cache.latent[i], idx, cfg.softmax_scale, r, sink=L.sink_all)
-                o = pc.tokens_to_heads(o_tok.contiguous()) if self.on_gpu else pc.tokens_to_heads(o_tok)
+                o = A.sparse_mla(q_tok, cache.latent[i], idx, cfg.softmax_scale, r, sink=L.sink_all)
+                if not tok_major:
+                    o = pc.tokens_to_heads(o.contiguous()) if self.on_gpu else pc.tokens_to_heads(o)
             else:
                 o = A.sparse_mla(q.contiguous(), cache.latent[i], idx, cfg.softmax_scale, r, sink=L.sink)
             o = o.to(self.act_dtype).contiguous() if self.on_gpu else o.float().contiguous()
-            C.rope_(o, r - dr, dr, self.cos_sin, pos_q, inverse=True)
-        return o
+            C.rope_(o, r - dr, dr, self.cos_sin, fb.pos[lo:hi] if tok_major else pos_q, inverse=True)
+        return o, tok_major
 
     def _attn_decode(self, i, q, fb, cache, idx_l, dp: bool = False):
         cfg, L, pc = self.cfg, self.layers[i], self.pctx
@@ -676,12 +693,17 @@ class DeepseekModel:
                 q_tok = pc.heads_to_tokens(qf)                                      # [n_r, H, r + dr]
                 o_tok = A.sparse_mla(q_tok, cache.latent[i], idx.contiguous(), cfg.softmax_scale, r,
                                      sink=L.sink_all)
+            if self.o_a2a:
+                # the owner keeps its tokens' outputs: every head's value projection here, no way back
+                with region("attn.absorb_o"):
+                    return head_bmm(o_tok, L.w_uv_all), True                         # [n_r, H, dv]
+            with region("attn.core_decode"):
                 o_lat = pc.tokens_to_heads(o_tok)                                   # [T, Hl, r]
         else:
             with region("attn.core_decode"):
                 o_lat = A.sparse_mla(qf, cache.latent[i], idx.contiguous(), cfg.softmax_scale, r, sink=L.sink)
         with region("attn.absorb_o"):
-            return head_bmm(o_lat, L.w_uv)                                           # [T, Hl, dv]
+            return head_bmm(o_lat, L.w_uv), False                                    # [T, Hl, dv]
 
     # ------------------------------------------------------------------------------------------------------------------
     # FFN

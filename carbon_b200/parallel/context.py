@@ -32,6 +32,9 @@ class ParallelCtx:
     # DP attention: every rank runs attention for its own sequences with all heads (tp = 1 for attention weights,
     # no attention collectives); MoE stays expert-parallel over all ranks
     attn_dp: bool = False
+    # TP attention output: heads -> tokens all-to-all of the per-head outputs, then the whole output projection on each
+    # token's owner (wo replicated), instead of the row-parallel projection + reduce-scatter of [T, hidden] partials
+    oproj_a2a: bool = False
     group: Optional[object] = None   # torch.distributed process group (NCCL) when world > 1
     bounds: Optional[list] = None    # token shard bounds of the current batch ([0, T] on one rank)
 

@@ -48,12 +48,15 @@ def split_bounds(lengths: List[int], world: int) -> List[int]:
 
 
 class DistCtx(ParallelCtx):
-    def __init__(self, rank: int, world: int, group=None, attn_dp: bool = False):
+    def __init__(self, rank: int, world: int, group=None, attn_dp: bool = False, oproj_a2a: bool = False):
         """attn_dp: data-parallel attention (each rank attends over its own sequences with all heads) instead of
-        tensor-parallel attention over heads; MoE is expert-parallel either way."""
+        tensor-parallel attention over heads; MoE is expert-parallel either way.  oproj_a2a (TP attention): the
+        per-head outputs go to each token's owner by an all-to-all and the owner runs the whole output projection,
+        instead of a row-parallel projection whose [T, hidden] partial sums are reduce-scattered (the NCCL baseline
+        keeps the reduce-scatter by default)."""
         super().__init__(rank=rank, world=world, tp=1 if attn_dp else world, ep=world,
                          tp_rank=0 if attn_dp else rank, ep_rank=rank, vocab_parallel=True, attn_dp=attn_dp,
-                         group=group)
+                         oproj_a2a=oproj_a2a and not attn_dp and world > 1, group=group)
         self.bounds: Optional[List[int]] = None
 
     # -- shard bookkeeping ----------------------------------------------------------------------------------------

@@ -31,8 +31,8 @@ from .symm import SymmHeap
 class FusedCtx(DistCtx):
     def __init__(self, rank: int, world: int, group=None, heap_bytes: int = 4 << 30, max_tokens: int = 8192,
                  max_seq: int = 4096, moe_capacity: float = 1.6, barrier_timeout_s: float = 20.0,
-                 attn_dp: bool = False):
-        super().__init__(rank, world, group, attn_dp=attn_dp)
+                 attn_dp: bool = False, oproj_a2a: bool = True):
+        super().__init__(rank, world, group, attn_dp=attn_dp, oproj_a2a=oproj_a2a)
         self.device = torch.device("cuda", torch.cuda.current_device())
         self.heap = SymmHeap(heap_bytes, rank, world, group, self.device)
         self.max_tokens = max_tokens

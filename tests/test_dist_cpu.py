@@ -27,13 +27,14 @@ def _prompts(cfg, variant="v3"):
     g = torch.Generator().manual_seed(1)
     # "skewed": prefill shards by tokens (rank 0: the 200-token prompt; rank 1: the short ones) but decode shards by
     # rows (rank 0: requests 0-1), so request 1 decodes on a rank that did not prefill it
-    lens = (200, 10, 10) if variant == "skewed" else (64, 50, 70)
+    lens = (200, 10, 10) if variant.startswith("skewed") else (64, 50, 70)
     return [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in lens]
 
 
 def _cfg(variant):
     from carbon_b200.config import tiny_v4_config
 
+    variant = variant.replace("+a2a", "")
     if variant == "v4_late":
         return tiny_v4_config().replace(n_layers=3, index_sources=(1,), late_layer_start=2, late_replay=24)
     if variant == "v3_plain":
@@ -53,7 +54,7 @@ def _worker(rank, world, port, q, attn_dp=False, variant="v3"):
         cfg = _cfg(variant)
         w = init_weights(cfg, seed=0)
         eng = Engine(cfg, device="cpu", source=WeightSource(cfg, state=w), num_pages=32, page_size=16,
-                     pctx=DistCtx(rank, world, attn_dp=attn_dp))
+                     pctx=DistCtx(rank, world, attn_dp=attn_dp, oproj_a2a=variant.endswith("+a2a")))
         outs, hist = eng.generate(_prompts(cfg, variant), max_new_tokens=6, return_logits=True)
         q.put((rank, outs, [h.numpy().copy() for h in hist]))
     finally:
@@ -63,7 +64,10 @@ def _worker(rank, world, port, q, attn_dp=False, variant="v3"):
 @pytest.mark.parametrize("world,attn_dp,variant", [(2, False, "v3"), (2, True, "v3"), (2, False, "v4"),
                                                    (2, True, "v4"), (2, False, "v4_late"), (2, True, "v4_late"),
                                                    (2, True, "skewed"), (2, False, "skewed"), (4, False, "v3"),
-                                                   (4, True, "v3"), (2, False, "v3_plain")])
+                                                   (4, True, "v3"), (2, False, "v3_plain"),
+                                                   # TP attention with the head -> token all-to-all output projection
+                                                   (2, False, "v3+a2a"), (4, False, "v3+a2a"), (2, False, "v4+a2a"),
+                                                   (2, False, "v4_late+a2a"), (2, False, "skewed+a2a")])
 def test_tp_ep_engine_matches_single_rank(world, attn_dp, variant):
     cfg = _cfg(variant)
     w = init_weights(cfg, seed=0)
