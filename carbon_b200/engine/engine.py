@@ -128,7 +128,7 @@ class Engine:
                  page_size: int = 64, model: Optional[DeepseekModel] = None, cuda_graphs: bool = False,
                  graph_buckets: Sequence[int] = (1, 2, 4, 8, 16, 32, 64, 128, 256), pctx=None, fp8: bool = True,
                  prefix_cache: bool = False, record_expert_load: bool = False, balance_dp: bool = False,
-                 dp_owner_kv: bool = False):
+                 dp_owner_kv: bool = False, owner_kv: bool = False):
         self.cfg = cfg
         self.device = torch.device(device)
         self.model = model if model is not None else DeepseekModel(cfg, source or WeightSource(cfg), device,
@@ -150,17 +150,22 @@ class Engine:
         self.stager = PinnedStager(self.device)
         # DP attention: place prefill sequences and decode rows on ranks by a FLOP cost model instead of by count
         self.balance_dp = balance_dp
-        # DP attention with owner-only KV: every request has a home rank (chosen by the cost-model planner at its
-        # prefill) that alone allocates and writes its KV pages; its prefill and decode rows always run there, and
-        # decode pads each rank's rows to the busiest rank's count (fixed per-rank blocks for the decode graphs).
-        # Each rank then holds only its own requests' KV (the reference's DP-attention layout).
+        # Owner-only KV: every request has a home rank (chosen by the cost-model planner at its prefill) that alone
+        # allocates and writes its KV pages; its prefill and decode rows always run there, and decode pads each
+        # rank's rows to the busiest rank's count (fixed per-rank blocks for the decode graphs).  Each rank then
+        # holds only its own requests' KV.  DP attention reads the cache on the home rank by construction; TP
+        # attention does too, because its cache-reading core runs token-parallel after the heads -> tokens
+        # exchange (the prefill core of MLA works on the gathered new rows, not on the cache).
+        # (`dp_owner_kv` is the older name of the same switch.)
         pc = self.model.pctx
-        self.dp_owner_kv = bool(dp_owner_kv and pc.world > 1 and pc.attn_dp)
-        if dp_owner_kv and not self.dp_owner_kv:
-            raise ValueError("dp_owner_kv needs DP attention on several ranks")
-        if self.dp_owner_kv and prefix_cache:
-            raise ValueError("dp_owner_kv does not combine with the prefix cache (pages are per home rank)")
-        self.model.dp_owner_kv = self.dp_owner_kv
+        want = dp_owner_kv or owner_kv
+        self.owner_kv = bool(want and pc.world > 1 and (pc.attn_dp or hasattr(pc, "heads_to_tokens")))
+        if want and not self.owner_kv:
+            raise ValueError("owner-only KV needs several ranks (DP attention, or TP attention with a heads -> "
+                             "tokens exchange)")
+        if self.owner_kv and prefix_cache:
+            raise ValueError("owner-only KV does not combine with the prefix cache (pages are per home rank)")
+        self.model.owner_kv = self.owner_kv
         if record_expert_load and cfg.n_routed_experts:
             from ..parallel.placement import ExpertLoad
 
@@ -185,14 +190,14 @@ class Engine:
 
     def pages_for(self, r: Request, n_tokens: int) -> int:
         """New KV pages request ``r`` needs to hold ``n_tokens`` tokens (on its home rank, with owner-only KV)."""
-        held = r.n_pages if self.dp_owner_kv else len(r.pages)
+        held = r.n_pages if self.owner_kv else len(r.pages)
         return max(0, (n_tokens + self.page_size - 1) // self.page_size - held)
 
     def pages_available(self, home: Optional[int] = None) -> int:
         """Pages an allocation can get now: free pages plus cached prefix pages that only the prefix cache holds.
         With owner-only KV, the free pages of rank ``home``, counted from the page counts of the requests it owns
         (the same number on every rank, so every rank takes the same scheduling decisions)."""
-        if self.dp_owner_kv:
+        if self.owner_kv:
             held = sum(r.n_pages for r in self._live.values() if r.home == home)
             return self.cache.alloc.num_pages() - 1 - held
         a = self.cache.alloc
@@ -202,7 +207,7 @@ class Engine:
         return n
 
     def _mine(self, r: Request) -> bool:
-        return not self.dp_owner_kv or r.home == self.model.pctx.rank
+        return not self.owner_kv or r.home == self.model.pctx.rank
 
     def _table(self, r: Request, n_tokens: int) -> List[int]:
         """Page table used for ``r``'s metadata on this rank: its pages, or (owner-only KV, another rank's request)
@@ -212,7 +217,7 @@ class Engine:
         return [self._scratch[0]] * max(1, (n_tokens + self.page_size - 1) // self.page_size)
 
     def _ensure_pages(self, r: Request, n_tokens: int):
-        if self.dp_owner_kv:
+        if self.owner_kv:
             need = self.pages_for(r, n_tokens)
             if need > 0 and self._mine(r):
                 r.pages += list(self.cache.alloc.alloc(need))
@@ -270,18 +275,18 @@ class Engine:
         with a cached prefix (chunked prefill, prefix reuse) continue through per-row attention over the cache."""
         if any(r.n_cached > 0 for r in reqs):
             return self._prefill_rows(reqs, [r.seq_len - r.n_cached for r in reqs])
-        if self.dp_owner_kv or (self._dp_balanced() and len(reqs) > 1):
+        if self.owner_kv or (self._dp_balanced() and len(reqs) > 1):
             from ..parallel.balance import plan_prefill
 
             world = self.model.pctx.world
-            if self.dp_owner_kv and all(r.home >= 0 for r in reqs):      # homes chosen by the caller (scheduler)
+            if self.owner_kv and all(r.home >= 0 for r in reqs):      # homes chosen by the caller (scheduler)
                 order = sorted(range(len(reqs)), key=lambda i: (reqs[i].home, i))
                 bounds = [0]
                 for h in range(world):
                     bounds.append(bounds[-1] + sum(r.seq_len for r in reqs if r.home == h))
                 return _unpermute(self._prefill_full([reqs[i] for i in order], bounds), order)
             order, bounds, _ = plan_prefill(self.cfg, [r.seq_len for r in reqs], world)
-            if self.dp_owner_kv:                # the planned rank becomes each request's home
+            if self.owner_kv:                # the planned rank becomes each request's home
                 start = 0
                 for i in order:
                     reqs[i].home = max(k for k in range(len(bounds) - 1) if bounds[k] <= start)
@@ -346,7 +351,7 @@ class Engine:
         with each rank's block padded to the busiest rank's count (pad rows on the scratch page).  Returns the
         flat (tables, lengths, ids, late) lists and the position of each request's first row."""
         tables, lens, ids, late, first = [], [], [], [], [0] * len(reqs)
-        if self.dp_owner_kv:
+        if self.owner_kv:
             world = self.model.pctx.world
             groups = [[b for b, r in enumerate(reqs) if r.home == h] for h in range(world)]
             width = max(sum(len(rows[b]) for b in g) for g in groups)
@@ -373,7 +378,7 @@ class Engine:
         (keys: the request's cached tokens and the rows before it).  Returns logits [B, V] of each request's last
         row of this step.  With owner-only KV the rows are grouped by home rank (requests without one get it from
         the cost-model plan) and each rank's block is padded to the busiest rank's row count."""
-        if self.dp_owner_kv:
+        if self.owner_kv:
             fresh = [b for b, r in enumerate(reqs) if r.home < 0]
             if fresh:                               # first chunk: the cost-model plan picks the home rank
                 from ..parallel.balance import plan_prefill
@@ -409,7 +414,7 @@ class Engine:
 
     def decode(self, reqs: List[Request], next_tokens: Sequence[int]) -> torch.Tensor:
         """Append one token per request and run it; returns logits [B, V]."""
-        if self.dp_owner_kv:
+        if self.owner_kv:
             return self._decode_owner(reqs, next_tokens)
         if self._dp_balanced() and len(reqs) > 1:
             from ..parallel.balance import plan_rows, seq_cost
@@ -503,7 +508,7 @@ class Engine:
         KV rows of rejected drafts are simply overwritten later (positions are slot-addressed)."""
         rows = []
         for r, t, d in zip(reqs, last_tokens, drafts):
-            if self.dp_owner_kv and not 0 <= r.home < self.model.pctx.world:
+            if self.owner_kv and not 0 <= r.home < self.model.pctx.world:
                 raise RuntimeError(f"request {r.rid} has no home rank (prefill it on this engine first)")
             base = r.seq_len
             seq = [int(t)] + [int(x) for x in d]
@@ -515,7 +520,7 @@ class Engine:
         # verify rows are decode rows (one token each, its own key list): a captured decode graph of a large enough
         # bucket serves them (the reference captures verify buckets of 6-row multiples).  Owner-only KV runs them
         # eagerly: its per-rank padded blocks need the exact row count.
-        bucket = self._bucket(n) if self.cuda_graphs and not self.dp_owner_kv else None
+        bucket = self._bucket(n) if self.cuda_graphs and not self.owner_kv else None
         out_loc, key_slots, n_keys, pos = decode_metadata(rows_pt, rows_len, self.page_size, bucket or n)
         dev = self.device
         with self.metrics.step("verify", n, len(reqs)):

@@ -64,10 +64,10 @@ class Scheduler:
         it launches work that would wait for it; watchdog (``utils.health.Watchdog``): a step that overruns its
         limit raises ``StepStalled``; check_device: read the cross-rank kernels' status word after every step."""
         self.eng = engine
-        # DP attention with owner-only KV: each admitted request gets a home rank (the one with the most free
+        # Owner-only KV: each admitted request gets a home rank (the one with the most free
         # pages), pages are budgeted per home rank, and preemption picks its victims among the requests of the
         # rank that runs short.  Every rank computes the same decisions.
-        self.owner = bool(getattr(engine, "dp_owner_kv", False))
+        self.owner = bool(getattr(engine, "owner_kv", False))
         self.world = engine.model.pctx.world
         self.heartbeat = heartbeat
         self.watchdog = watchdog

@@ -155,7 +155,7 @@ class DeepseekModel:
         self.fp8 = fp8
         self.trace = None          # set to a list to record (name, tensor) at sublayer boundaries (debugging)
         self.expert_load = None    # placement.ExpertLoad: per-layer routing counts for expert rebalancing
-        self.dp_owner_kv = False   # DP attention: only a request's home rank caches its KV (no all-gather)
+        self.owner_kv = False      # only a request's home rank caches its KV (no all-gather of the new rows)
         self._side = None          # side stream of the shared expert
         self._dsa = {}
         cfg.validate()
@@ -459,9 +459,19 @@ class DeepseekModel:
                 idx_l = self.indexer_qkw(i, h, q_lat_l, pos_l)
         q_lat_a = q_lat_l.to(self.act_dtype) if self.on_gpu else q_lat_l
         out_loc = fb.out_loc
-        if dp and self.dp_owner_kv:
+        if dp and self.owner_kv:
             # each request's rows always run on its home rank: this rank caches only its own rows
             q_lat, latent, latent_c = q_lat_a, latent_l, latent_l
+            idx_k = idx_l[1] if idx_l is not None else None
+            out_loc = fb.out_loc[lo:hi]
+        elif self.owner_kv:
+            # TP attention, owner-only KV: the cache-reading core runs token-parallel on each token's home rank, so
+            # only the home rank writes the token's rows; the other ranks need the new latent rows only for the MLA
+            # prefill core (k / v of every token from wkv_b)
+            with region("tp.gather"):
+                q_lat = pc.gather_rows(q_lat_a)
+                latent = pc.gather_rows(latent_l) if fb.is_prefill and cfg.attn_kind == "mla" else None
+            latent_c = latent_l
             idx_k = idx_l[1] if idx_l is not None else None
             out_loc = fb.out_loc[lo:hi]
         elif dp:

@@ -13,7 +13,7 @@ placed whole: LPT (longest-processing-time first) over ranks for prefill, where 
 plan; and, for decode, a capacity-constrained LPT that keeps the per-rank row counts (so captured decode graphs keep
 their shapes) and only chooses which rows each rank runs.  By default decode KV is in every DP rank's cache (new
 rows are all-gathered), so a request can move between ranks from one step to the next at no transfer cost; with
-owner-only KV (``Engine(dp_owner_kv=True)``) the prefill plan fixes each request's home rank instead.
+owner-only KV (``Engine(owner_kv=True)``) the prefill plan fixes each request's home rank instead.
 """
 from __future__ import annotations
 

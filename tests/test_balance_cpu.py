@@ -2,6 +2,8 @@
 prefill sequences and decode rows by the plan serves exactly the same tokens as one that splits by count."""
 import socket
 
+import pytest
+
 import torch
 
 from carbon_b200.config import deepseek_v3_config, tiny_config
@@ -115,7 +117,15 @@ def test_balanced_dp_engine_serves_the_same_tokens():
             assert (torch.tensor(a) - torch.tensor(b)).abs().max() < 1e-3
 
 
-def _owner_worker(rank, world, port, q):
+def _owner_cfg(mode):
+    if "v4" in mode:
+        from carbon_b200.config import tiny_v4_config
+
+        return tiny_v4_config().replace(n_layers=3, index_sources=(1,), engram_layers=())
+    return tiny_config()
+
+
+def _owner_worker(rank, world, port, q, mode="dp"):
     import os
     from datetime import timedelta
 
@@ -130,10 +140,10 @@ def _owner_worker(rank, world, port, q):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
     try:
-        cfg = tiny_config()
+        cfg = _owner_cfg(mode)
         w = init_weights(cfg, seed=0)
         e = Engine(cfg, device="cpu", source=WeightSource(cfg, state=w), num_pages=48, page_size=16,
-                   pctx=DistCtx(rank, world, attn_dp=True), dp_owner_kv=True)
+                   pctx=DistCtx(rank, world, attn_dp=mode == "dp", oproj_a2a="a2a" in mode), owner_kv=True)
         reqs = [e.add_request(p) for p in _prompts(cfg)]
         logits = e.prefill(reqs)
         hist = [logits.tolist()]
@@ -168,17 +178,19 @@ def _owner_worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-def test_dp_owner_kv_matches_single_rank_and_splits_pages():
-    """Owner-only KV (2 DP ranks): each request's KV lives on its home rank only, yet the served tokens and logits
-    equal the single-rank engine's, with whole-prompt and chunked prefill and with speculative verify; the ranks'
-    page counts add up to the single rank's."""
+@pytest.mark.parametrize("mode", ["dp", "tp", "tp_a2a", "tp_a2a_v4"])
+def test_owner_kv_matches_single_rank_and_splits_pages(mode):
+    """Owner-only KV on 2 ranks (DP attention, or TP attention whose cache-reading core runs token-parallel): each
+    request's KV lives on its home rank only, yet the served tokens and logits equal the single-rank engine's, with
+    whole-prompt and chunked prefill and with speculative verify; the ranks' page counts add up to the single
+    rank's."""
     import torch.multiprocessing as mp
 
     from carbon_b200.engine.engine import Engine
     from carbon_b200.models.weights import WeightSource
     from carbon_b200.ref.model import init_weights
 
-    cfg = tiny_config()
+    cfg = _owner_cfg(mode)
     w = init_weights(cfg, seed=0)
     single = Engine(cfg, device="cpu", source=WeightSource(cfg, state=w), num_pages=48, page_size=16)
     ref_out, ref_hist = single.generate(_prompts(cfg), 5, return_logits=True)
@@ -188,7 +200,7 @@ def test_dp_owner_kv_matches_single_rank_and_splits_pages():
     s.close()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    ps = [ctx.Process(target=_owner_worker, args=(r, 2, port, q)) for r in range(2)]
+    ps = [ctx.Process(target=_owner_worker, args=(r, 2, port, q, mode)) for r in range(2)]
     for p in ps:
         p.start()
     res = sorted([q.get(timeout=300) for _ in range(2)], key=lambda x: x[0])
@@ -230,7 +242,7 @@ def _owner_sched_worker(rank, world, port, q, num_pages, prefill_tokens):
         cfg = tiny_config()
         w = init_weights(cfg, seed=0)
         e = Engine(cfg, device="cpu", source=WeightSource(cfg, state=w), num_pages=num_pages, page_size=16,
-                   pctx=DistCtx(rank, world, attn_dp=True), dp_owner_kv=True)
+                   pctx=DistCtx(rank, world, attn_dp=True), owner_kv=True)
         s = Scheduler(e, prefill_tokens=prefill_tokens)
         ids = [s.submit(p, 40) for p in _sched_prompts(cfg)]
         out = s.run()
