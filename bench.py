@@ -51,6 +51,11 @@ def parse():
                          "(one per rank)")
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"],
                     help="multi-GPU data movement: our NVLink kernels (fused) or the NCCL baseline")
+    ap.add_argument("--oproj", default="a2a", choices=["a2a", "rs"],
+                    help="TP attention output: heads -> tokens all-to-all + whole projection on the token's owner "
+                         "(a2a) or row-parallel projection + reduce-scatter (rs)")
+    ap.add_argument("--replicated-kv", action="store_true",
+                    help="N>1: every rank caches every request's KV (default: only each request's home rank does)")
     ap.add_argument("--attn", default="tp", choices=["tp", "dp"],
                     help="attention parallelism for N>1: tensor-parallel over heads (the headline configuration) or "
                          "data-parallel over each rank's own sequences")
@@ -149,7 +154,7 @@ def main():
     if world > 1:
         import datetime
 
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=dev)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
     ext()
     cfg = PRESETS[args.config]()
     if args.layers:
@@ -166,12 +171,17 @@ def main():
         from carbon_b200.parallel.fused import FusedCtx
 
         max_tokens = max(P * S, B) * world
-        pctx = FusedCtx(rank, world, heap_bytes=heap_bytes(cfg, world, max_tokens, S), max_tokens=max_tokens,
-                        max_seq=S, attn_dp=args.attn == "dp")
+        a2a = args.oproj == "a2a" and args.attn == "tp"
+        pctx = FusedCtx(rank, world, heap_bytes=heap_bytes(cfg, world, max_tokens, S, a2a), max_tokens=max_tokens,
+                        max_seq=S, attn_dp=args.attn == "dp", oproj_a2a=a2a)
     mem = torch.cuda.get_device_properties(dev).total_memory
     page = 64
-    dec_pages = (B * world) * ((ctx + args.decode_steps * (args.warmup + args.steps) * 2 + 2 * page) // page + 1)
-    pf_pages = (P * world) * (S // page + 2)
+    # owner-only KV (N > 1): a rank holds pages only for the requests whose home it is (B per GPU at decode, about
+    # P per GPU at prefill); replicated KV holds every request's pages on every rank
+    owner_kv = world > 1 and not args.replicated_kv
+    kv_ranks = 1 if owner_kv else world
+    dec_pages = (B * kv_ranks) * ((ctx + args.decode_steps * (args.warmup + args.steps) * 2 + 2 * page) // page + 1)
+    pf_pages = (P * kv_ranks + (P if owner_kv else 0)) * (S // page + 2)     # owner: room for an uneven plan
     num_pages = max(dec_pages, pf_pages) + 8
     from carbon_b200.engine.kv_cache import PagedLatentCache
 
@@ -187,8 +197,10 @@ def main():
     B = B * world
     pages_needed = num_pages
     graphs = world == 1 or args.comm == "fused"
+    # decode graphs: one bucket of the per-rank block (owner-only KV pads each home rank's rows to a fixed block) or
+    # of the whole batch
     eng = Engine(cfg, device=dev, source=src, num_pages=pages_needed, page_size=page, cuda_graphs=graphs,
-                 graph_buckets=(B,), pctx=pctx)
+                 graph_buckets=(B // world if owner_kv else B,), pctx=pctx, owner_kv=owner_kv)
     torch.cuda.synchronize()
     init_s = time.time() - t0
     gen = torch.Generator().manual_seed(1234)     # SPMD: every rank builds the same requests
@@ -255,8 +267,10 @@ def main():
 
     # ---------------- decode (CUDA graphs, context `ctx`) ----------------
     reqs = []
-    for _ in range(B):
+    for j in range(B):
         r = eng.add_request(torch.randint(0, cfg.vocab_size, (ctx,), generator=gen).tolist())
+        if owner_kv:
+            r.home = j // (B // world)          # B / N requests per home rank
         eng._ensure_pages(r, r.seq_len)
         r.n_cached = ctx          # cache rows are synthetic: decode cost depends on context length, not content
         reqs.append(r)
@@ -328,7 +342,7 @@ def main():
             "config": {"model": f"{args.config} ({cfg.n_layers} layers, hidden {cfg.hidden_size}, "
                                 f"{cfg.n_routed_experts} experts top-{cfg.n_activated_experts})",
                        "global_batch": P, "seq_len": S, "decode_batch": B, "context": ctx,
-                       "parallelism": pctx_name(pctx, world),
+                       "parallelism": pctx_name(pctx, world, owner_kv),
                        "weights": (f"{sets} distinct MoE-layer weight sets cycled over {n_moe} MoE layers "
                                    "(every layer still runs; the full untied model needs 8 GPUs)") if tied
                        else "all layers distinct", "l2": "inputs (weights) larger than L2",
@@ -339,19 +353,29 @@ def main():
         dist.destroy_process_group()
 
 
-def pctx_name(p, world):
+def pctx_name(p, world, owner_kv=False):
     if world == 1:
         return "single GPU"
     kind = "NVLink peer-memory kernels" if type(p).__name__ == "FusedCtx" else "NCCL baseline"
-    attn = f"dp{world} attention" if getattr(p, "attn_dp", False) else f"tp{p.tp} attention"
-    return f"{attn} + ep{p.ep} MoE, sequence-sharded residual ({kind})"
+    if getattr(p, "attn_dp", False):
+        attn = f"dp{world} attention"
+    else:
+        attn = f"tp{p.tp} attention" + (" (output projection after a heads->tokens all-to-all)"
+                                         if getattr(p, "oproj_a2a", False) else "")
+    kv = "KV on each request's home rank" if owner_kv else "KV replicated on every rank"
+    return f"{attn} + ep{p.ep} MoE, sequence-sharded residual, {kv} ({kind})"
 
 
-def heap_bytes(cfg, world, max_tokens, max_seq):
-    """Symmetric-heap size: reduce-scatter slots, MoE receive/output rows, gathers, vocab shard, slack."""
+def heap_bytes(cfg, world, max_tokens, max_seq, oproj_a2a=True):
+    """Symmetric-heap size: reduce-scatter slots (or heads -> tokens buffers), MoE receive/output rows, gathers,
+    vocab shard, slack."""
     D = cfg.hidden_size
     max_local = min(max_tokens, (max_tokens + world - 1) // world + max_seq)
-    rs = 2 * world * max_local * D * 2
+    pow2 = 1 << max(4, (max_local - 1).bit_length())          # gather slots grow in powers of two rows
+    if oproj_a2a:
+        rs = 2 * pow2 * cfg.n_heads * cfg.head_out_dim * 2    # double-buffered per-head outputs of this rank's tokens
+    else:
+        rs = 2 * world * max_local * D * 2
     cap = int(max_local * cfg.n_activated_experts * 1.6) + (cfg.n_routed_experts // world) * 256 + 256
     cap2 = int((max_local + 1) // 2 * cfg.n_activated_experts * 1.6) + (cfg.n_routed_experts // world) * 256 + 256
     moe = (cap + cap2) * (D * 3 + D // 32) + (2 << 20)       # buffer sets of a whole call and of a second chunk

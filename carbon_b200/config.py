@@ -57,6 +57,10 @@ class ModelConfig:
     # indexer q and k in fp8 e4m3 with one UE8M0 scale per 128-dim row (per head for q), the DeepSeek-V3.2 indexer
     # precision: the prefill logits run as block-scaled fp8 tcgen05 MMAs; decode sees the same rounded values
     index_fp8: bool = False
+    # MLA prefill over sequences longer than this runs as absorbed sparse attention over each query's top-k cached
+    # latent rows (cost linear in length at a fixed top-k) instead of the dense causal kernel with a DSA key mask
+    # (cheaper for short prompts: 320 vs 1088 MACs per key and head); 0 = always the dense kernel
+    sparse_prefill_min: int = 12288
     # per-head learned attention sink: one extra logit in each softmax denominator (attn.sink [n_heads] fp32)
     attn_sink: bool = False
     # attention kind.  "mla": q/k = [nope | RoPE] per head, keys and values up-projected from the kv latent (wkv_b);

@@ -384,6 +384,18 @@ void indexer_decode_logits(torch::Tensor q, torch::Tensor w, torch::Tensor kc, t
                                logits.data_ptr<float>(), nullptr, cur_stream()));
 }
 
+// Causal top-k of one prefill sequence block: logits [Tq, ldo] (row t: keys 0..row0+t), seq_slots [L] -> out [Tq, k].
+void topk_causal_slots(torch::Tensor logits, torch::Tensor seq_slots, int64_t row0, torch::Tensor out) {
+  CHECK_CUDA(logits); CHECK_DT(logits, at::kFloat); CHECK_DT(seq_slots, at::kInt); CHECK_DT(out, at::kInt);
+  CHECK_CONTIG(seq_slots); CHECK_CONTIG(out);
+  TORCH_CHECK(logits.stride(1) == 1 && out.size(0) == logits.size(0));
+  const int T = logits.size(0), L = seq_slots.numel();
+  TORCH_CHECK(row0 + T <= L && logits.size(1) >= row0 + T, "causal rows beyond the sequence");
+  c10::cuda::CUDAGuard g(logits.device());
+  CK(cb::topk_slots(logits.data_ptr<float>(), logits.stride(0), seq_slots.data_ptr<int>(), 0, nullptr, int(row0), T,
+                    L, out.size(1), out.data_ptr<int>(), cur_stream()));
+}
+
 void indexer_topk(torch::Tensor q, torch::Tensor w, torch::Tensor kc, torch::Tensor key_slots, torch::Tensor n_keys,
                   torch::Tensor out) {
   CHECK_CUDA(q); CHECK_CONTIG(out); CHECK_DT(out, at::kInt);
@@ -431,4 +443,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("engram_gate", &engram_gate);
   m.def("indexer_topk", &indexer_topk);
   m.def("indexer_decode_logits", &indexer_decode_logits);
+  m.def("topk_causal_slots", &topk_causal_slots);
 }

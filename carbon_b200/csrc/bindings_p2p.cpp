@@ -20,11 +20,14 @@ cudaError_t p2p_a2a_heads(const void* src, const int* bounds_dev, int world, int
                           int C, int mode, int max_rows, cudaStream_t s);
 cudaError_t moe_count(const int* ids, int Tk, int E, int world, int my_rank, const uint64_t* cnt_ptrs,
                       int* pair_rank, cudaStream_t s);
-cudaError_t moe_owner_layout(const int* cnt, int world, int El, int max_blocks, int* src_off, int* m_block_expert,
-                             int* num_blocks, cudaStream_t s, int align);
+cudaError_t moe_layout(const int* cnt, int world, int E, int my_rank, int max_blocks, int align, int* my_off,
+                       int* m_block_expert, int* num_blocks, cudaStream_t s);
 cudaError_t moe_dispatch(const void* x, int T, int D, const int* ids, int k, int El, int my_rank,
                          const int* pair_rank, const uint64_t* recv_ptrs, const uint64_t* sf_ptrs,
-                         const uint64_t* off_ptrs, int cap, int* pos_out, int* status, cudaStream_t s);
+                         const int* my_off, const uint64_t* rinfo_ptrs, int cap, int* pos_out, int* status,
+                         cudaStream_t s);
+cudaError_t moe_combine_slots(const void* slots, int T, int D, const int* pos, const float* w, int k, const void* add,
+                              void* out, cudaStream_t s);
 cudaError_t moe_combine_pull(const uint64_t* y_ptrs, int T, int D, const int* ids, const int* pos, const float* w,
                              int k, int El, const void* add, void* out, cudaStream_t s);
 cudaError_t embed_peer(const uint64_t* table_ptrs, int per, int world, const int* ids, int T, int D, int hc,
@@ -32,6 +35,10 @@ cudaError_t embed_peer(const uint64_t* table_ptrs, int per, int world, const int
 cudaError_t gemm_fp8_scatter(const void* A, const void* B, const uint32_t* sfa, const uint32_t* sfb, int M, int N,
                              int K, const uint64_t* scatter_ptrs, const int* bounds, int world, int my_rank,
                              int slot_rows, int* status, int num_sms, cudaStream_t s);
+cudaError_t gemm_fp8_push(const void* A, const void* B, const uint32_t* sfa, const uint32_t* sfb, int M, int N, int K,
+                          int Nb, const int* m_block_expert, const int* num_m_blocks_dev, int max_m_blocks,
+                          const int* row_dst, const uint64_t* home_ptrs, int world, int* status, int num_sms,
+                          cudaStream_t s);
 }  // namespace cb
 
 namespace {
@@ -130,18 +137,44 @@ void moe_count(torch::Tensor ids, int64_t E, int64_t my_rank, torch::Tensor cnt_
   CKP(cb::moe_count(ids.data_ptr<int>(), ids.numel(), E, cnt_ptrs.numel(), my_rank, u64(cnt_ptrs),
                     pair_rank.data_ptr<int>(), stream()));
 }
-void moe_owner_layout(torch::Tensor cnt, int64_t world, int64_t El, torch::Tensor src_off,
-                      torch::Tensor m_block_expert, torch::Tensor num_blocks, int64_t align) {
-  CKP(cb::moe_owner_layout(cnt.data_ptr<int>(), world, El, m_block_expert.numel(), src_off.data_ptr<int>(),
-                           m_block_expert.data_ptr<int>(), num_blocks.data_ptr<int>(), stream(), int(align)));
+void moe_layout(torch::Tensor cnt, int64_t world, int64_t my_rank, torch::Tensor my_off, torch::Tensor m_block_expert,
+                torch::Tensor num_blocks, int64_t align) {
+  TORCH_CHECK(cnt.is_contiguous() && cnt.scalar_type() == at::kInt && cnt.size(0) == world);
+  CKP(cb::moe_layout(cnt.data_ptr<int>(), world, cnt.size(1), my_rank, m_block_expert.numel(), int(align),
+                     my_off.data_ptr<int>(), m_block_expert.data_ptr<int>(), num_blocks.data_ptr<int>(), stream()));
 }
 void moe_dispatch(torch::Tensor x, torch::Tensor ids, int64_t El, int64_t my_rank, torch::Tensor pair_rank,
-                  torch::Tensor recv_ptrs, torch::Tensor sf_ptrs, torch::Tensor off_ptrs, int64_t cap,
-                  torch::Tensor pos_out, torch::Tensor status) {
+                  torch::Tensor recv_ptrs, torch::Tensor sf_ptrs, torch::Tensor my_off,
+                  c10::optional<torch::Tensor> rinfo_ptrs, int64_t cap, torch::Tensor pos_out, torch::Tensor status) {
   TORCH_CHECK(x.is_contiguous() && x.scalar_type() == at::kBFloat16);
   CKP(cb::moe_dispatch(x.data_ptr(), x.size(0), x.size(1), ids.data_ptr<int>(), ids.size(1), El, my_rank,
-                       pair_rank.data_ptr<int>(), u64(recv_ptrs), u64(sf_ptrs), u64(off_ptrs), cap,
+                       pair_rank.data_ptr<int>(), u64(recv_ptrs), u64(sf_ptrs), my_off.data_ptr<int>(),
+                       rinfo_ptrs.has_value() && rinfo_ptrs->defined() ? u64(*rinfo_ptrs) : nullptr, cap,
                        pos_out.data_ptr<int>(), status.data_ptr<int>(), stream()));
+}
+void moe_combine_slots(torch::Tensor slots, torch::Tensor pos, torch::Tensor w, c10::optional<torch::Tensor> add,
+                       torch::Tensor out) {
+  TORCH_CHECK(slots.is_contiguous() && slots.scalar_type() == at::kBFloat16 && out.is_contiguous());
+  TORCH_CHECK(pos.is_contiguous() && w.is_contiguous() && slots.size(0) >= pos.numel());
+  CKP(cb::moe_combine_slots(slots.data_ptr(), out.size(0), out.size(1), pos.data_ptr<int>(), w.data_ptr<float>(),
+                            pos.size(1), add.has_value() && add->defined() ? add->data_ptr() : nullptr,
+                            out.data_ptr(), stream()));
+}
+// Grouped expert down-projection whose output rows are pushed to the tokens' home ranks (EP combine).
+void gemm_fp8_push(torch::Tensor A, torch::Tensor sfa, torch::Tensor B, torch::Tensor sfb, torch::Tensor mbe,
+                   torch::Tensor nb, int64_t n_per_group, torch::Tensor row_dst, torch::Tensor home_ptrs,
+                   torch::Tensor status) {
+  TORCH_CHECK(A.is_contiguous() && B.is_contiguous() && A.scalar_type() == at::kFloat8_e4m3fn &&
+              B.scalar_type() == at::kFloat8_e4m3fn && A.size(1) == B.size(1));
+  TORCH_CHECK(row_dst.numel() >= A.size(0) && row_dst.scalar_type() == at::kInt);
+  int dev;
+  cudaGetDevice(&dev);
+  int sms;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  CKP(cb::gemm_fp8_push(A.data_ptr(), B.data_ptr(), reinterpret_cast<const uint32_t*>(sfa.data_ptr()),
+                        reinterpret_cast<const uint32_t*>(sfb.data_ptr()), A.size(0), n_per_group, A.size(1),
+                        B.size(0), mbe.data_ptr<int>(), nb.data_ptr<int>(), mbe.numel(), row_dst.data_ptr<int>(),
+                        u64(home_ptrs), home_ptrs.numel(), status.data_ptr<int>(), sms, stream()));
 }
 void moe_combine_pull(torch::Tensor y_ptrs, torch::Tensor ids, torch::Tensor pos, torch::Tensor w, int64_t El,
                       c10::optional<torch::Tensor> add, torch::Tensor out) {
@@ -187,7 +220,9 @@ void register_p2p(pybind11::module_& m) {
   m.def("reduce_slots", &reduce_slots);
   m.def("p2p_a2a_heads", &p2p_a2a_heads);
   m.def("moe_count", &moe_count);
-  m.def("moe_owner_layout", &moe_owner_layout);
+  m.def("moe_layout", &moe_layout);
+  m.def("moe_combine_slots", &moe_combine_slots);
+  m.def("gemm_fp8_push", &gemm_fp8_push);
   m.def("moe_dispatch", &moe_dispatch);
   m.def("moe_combine_pull", &moe_combine_pull);
   m.def("embed_peer", &embed_peer);

@@ -400,6 +400,33 @@ cudaError_t gemm_fp8_scatter(const void* A, const void* B, const uint32_t* sfa, 
   return launch<KIND_MXF8, EPI_BF16_SCATTER, 128, 6, 2>(ta, tb, p, ceil_div(M, 128) * ceil_div(N, 128), num_sms, s);
 }
 
+// Grouped expert GEMM fused with the EP combine's data movement: fp8 A [M,K] (expert-sorted received rows, 256-row
+// aligned segments) x B [E*N, K]^T; each output row is stored over NVLink straight into its token's home-rank
+// combine slot (see EPI_BF16_PUSH), row-contiguous from the staged epilogue.  Padding rows (row_dst < 0) are skipped.
+cudaError_t gemm_fp8_push(const void* A, const void* B, const uint32_t* sfa, const uint32_t* sfb, int M, int N, int K,
+                          int Nb, const int* m_block_expert, const int* num_m_blocks_dev, int max_m_blocks,
+                          const int* row_dst, const uint64_t* home_ptrs, int world, int* status, int num_sms,
+                          cudaStream_t s) {
+  if (M <= 0 || N <= 0) return cudaSuccess;
+  if (K % 128 || N % 256 || (max_m_blocks & 1) || !m_block_expert || !row_dst) return cudaErrorInvalidValue;
+  CUtensorMap ta, tb, tsa, tsb;
+  if (!make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, K, 128, 128, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, Nb, K, 128, 64, CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_tmap_sf(&tsa, sfa, uint64_t(ceil_div(K, 512)) * ceil_div(M, 128), 1) ||
+      !make_tmap_sf(&tsb, sfb, uint64_t(ceil_div(K, 512)) * ceil_div(Nb, 128), 2))
+    return cudaErrorInvalidValue;
+  GemmParams p{};
+  p.M = M; p.N = N; p.K = K;
+  p.sfa = sfa; p.sfb = sfb;
+  p.sfa_row_blocks = ceil_div(M, 128);
+  p.sfb_row_blocks = ceil_div(Nb, 128);
+  p.ldo = N; p.status = status;
+  p.m_block_expert = m_block_expert; p.num_m_blocks_dev = num_m_blocks_dev;
+  p.row_dst = row_dst; p.scatter_ptrs = home_ptrs; p.scatter_world = world;
+  const int units = (max_m_blocks / 2) * ceil_div(N, 256);
+  return launch_pair<KIND_MXF8, EPI_BF16_PUSH, 2, 5>(ta, tb, tsa, tsb, p, units, num_sms, s);
+}
+
 // DSA indexer logits: keys [L, Di] bf16, q [Tq*H, Di] bf16, w [Tq, H] fp32 -> logits [Tq, ldo] fp32 (causal).
 cudaError_t indexer_logits(const void* keys, int L, const void* q, int Tq, int H, int Di, const float* w, float* out,
                            int ldo, bool causal, int* status, int num_sms, cudaStream_t s) {

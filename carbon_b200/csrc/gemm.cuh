@@ -22,8 +22,9 @@ namespace cb {
 
 enum GemmKind { KIND_MXF8 = 0, KIND_BF16 = 1 };
 // EPI_BF16_ROWS: EPI_BF16 with the output staged in shared memory and stored row-contiguous (pair kernel only)
+// EPI_BF16_PUSH: grouped expert GEMM whose output rows go straight to the routed token's home rank (EP combine)
 enum GemmEpi { EPI_BF16 = 0, EPI_SWIGLU_FP8 = 1, EPI_F32 = 2, EPI_INDEXER = 3, EPI_BF16_SCATTER = 4,
-               EPI_BF16_ROWS = 5 };
+               EPI_BF16_ROWS = 5, EPI_BF16_PUSH = 6 };
 
 struct GemmParams {
   int M, N, K;                 // N = per-expert N in grouped mode
@@ -52,6 +53,9 @@ struct GemmParams {
   int scatter_world, scatter_rank, scatter_rows;
   // optional: rows with row_valid[row] < 0 (expert-segment padding) are not written by the epilogue
   const int* row_valid;
+  // EPI_BF16_PUSH (expert GEMM -> EP combine over NVLink): row_dst[row] = (home rank << 24) | slot, or -1 for a
+  // padding row; the row is stored at scatter_ptrs[home] + slot * ldo (the home's [tokens * k, ldo] combine slots).
+  const int* row_dst;
 };
 
 template <int BLOCK_N>

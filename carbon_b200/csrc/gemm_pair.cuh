@@ -62,7 +62,8 @@ constexpr int gemm_pair_smem_bytes() {
   using C = PairCfg<KIND, PAIR, EPI>;
   return 1024 + STAGES * (C::TILE_A + C::TILE_B + C::SFA_BYTES + C::SFB_BYTES) + 8 * (2 * STAGES + 8) + 16 +
          2 * 2 * 128 * 4 +
-         (EPI == EPI_BF16_SCATTER || EPI == EPI_BF16_ROWS ? 16 + C::kEpiWarps * kScatterWarpBytes : 0) +
+         (EPI == EPI_BF16_SCATTER || EPI == EPI_BF16_ROWS || EPI == EPI_BF16_PUSH
+              ? 16 + C::kEpiWarps * kScatterWarpBytes : 0) +
          (EPI == EPI_SWIGLU_FP8 ? 16 + 4 * kSwiQuadBytes + 4 * 8 : 0);
 }
 
@@ -76,7 +77,8 @@ __global__ void __launch_bounds__(PairCfg<KIND, PAIR, EPI>::kThreads, 1)
   constexpr int BN = C::BN, BM = C::BM, BK = C::BK;
   constexpr bool kScaled = C::kScaled;
   constexpr int kMmaPerStage = BK / C::UMMA_K;
-  static_assert(EPI == EPI_BF16 || EPI == EPI_BF16_SCATTER || EPI == EPI_BF16_ROWS || EPI == EPI_SWIGLU_FP8 ||
+  static_assert(EPI == EPI_BF16 || EPI == EPI_BF16_SCATTER || EPI == EPI_BF16_ROWS || EPI == EPI_BF16_PUSH ||
+                    EPI == EPI_SWIGLU_FP8 ||
                     EPI == EPI_INDEXER,
                 "pair GEMM epilogues");
   static_assert(EPI != EPI_SWIGLU_FP8 || kScaled, "SwiGLU requant epilogue follows an fp8 GEMM");
@@ -318,7 +320,7 @@ __global__ void __launch_bounds__(PairCfg<KIND, PAIR, EPI>::kThreads, 1)
       const bool ovl_first = C::kOvl > 0 && s == 0 && h == 1;       // stage 0: local columns [224,256)
       const bool ovl_owner = C::kOvl > 0 && ((s == 0 && h == 1) || (s == 1 && h == 0));
 
-      if constexpr (EPI == EPI_BF16_SCATTER || EPI == EPI_BF16_ROWS) {
+      if constexpr (EPI == EPI_BF16_SCATTER || EPI == EPI_BF16_ROWS || EPI == EPI_BF16_PUSH) {
         // A row-per-lane store would put 32 rows' 16-byte pieces into one warp instruction: 32 small NVLink writes
         // (scatter: rows go to their owners' slots in peer HBM) or 32 partial-sector L2 writes (local rows).
         // Instead each 64-column slab of the warp's 32 rows is staged in shared memory and written back
@@ -332,6 +334,11 @@ __global__ void __launch_bounds__(PairCfg<KIND, PAIR, EPI>::kThreads, 1)
             while (r + 1 < p.scatter_world && row >= p.scatter_bounds[r + 1]) ++r;
             my_base = reinterpret_cast<__nv_bfloat16*>(p.scatter_ptrs[r]) +
                       (size_t(p.scatter_rank) * p.scatter_rows + (row - p.scatter_bounds[r])) * size_t(p.ldo);
+          } else if constexpr (EPI == EPI_BF16_PUSH) {
+            const int dst = p.row_dst[row];
+            const int home = dst >> 24;
+            if (dst >= 0 && home < p.scatter_world)
+              my_base = reinterpret_cast<__nv_bfloat16*>(p.scatter_ptrs[home]) + size_t(dst & 0xffffff) * p.ldo;
           } else {
             my_base = reinterpret_cast<__nv_bfloat16*>(p.out) + size_t(row) * p.ldo;
           }
@@ -527,7 +534,8 @@ __global__ void __launch_bounds__(PairCfg<KIND, PAIR, EPI>::kThreads, 1)
       }
       ++j;
     }
-    if constexpr (EPI == EPI_BF16_SCATTER) __threadfence_system();   // peer stores performed before any barrier
+    if constexpr (EPI == EPI_BF16_SCATTER || EPI == EPI_BF16_PUSH)
+      __threadfence_system();                                       // peer stores performed before any barrier
   }
 
   __syncthreads();

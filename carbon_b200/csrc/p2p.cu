@@ -156,9 +156,10 @@ cudaError_t reduce_slots(const void* slots, int world, int slot_rows, int n, int
 // EP MoE
 // ---------------------------------------------------------------------------------------------------------------
 // counts: one CTA per global expert scans this rank's (token, slot) pairs in order; pair_rank[i] = rank of pair i
-// among the pairs of its expert (token order, deterministic), and the expert's count is written into its owner's
-// count matrix cnt_ptrs[owner] -> int32 [world(src)][E_local].
-__global__ void moe_count_kernel(const int* __restrict__ ids, int Tk, int El, int my_rank,
+// among the pairs of its expert (token order, deterministic), and the expert's count is written into EVERY rank's
+// count matrix cnt_ptrs[r] -> int32 [world(src)][E], so that after one barrier each rank can lay out every owner's
+// receive buffer by itself (no second exchange of offsets).
+__global__ void moe_count_kernel(const int* __restrict__ ids, int Tk, int E, int world, int my_rank,
                                  const uint64_t* __restrict__ cnt_ptrs, int* __restrict__ pair_rank) {
   constexpr int kPer = 8;                  // consecutive pairs per thread per pass
   __shared__ int sw[32];
@@ -200,8 +201,8 @@ __global__ void moe_count_kernel(const int* __restrict__ ids, int Tk, int El, in
     base += sw[nw - 1];
     __syncthreads();
   }
-  if (threadIdx.x == 0) {
-    int* dst = reinterpret_cast<int*>(cnt_ptrs[e / El]) + my_rank * El + (e % El);
+  if (threadIdx.x < world) {
+    int* dst = reinterpret_cast<int*>(cnt_ptrs[threadIdx.x]) + my_rank * E + e;
     *dst = base;
     __threadfence_system();
   }
@@ -209,62 +210,76 @@ __global__ void moe_count_kernel(const int* __restrict__ ids, int Tk, int El, in
 
 cudaError_t moe_count(const int* ids, int Tk, int E, int world, int my_rank, const uint64_t* cnt_ptrs,
                       int* pair_rank, cudaStream_t s) {
-  const int El = E / world;
-  moe_count_kernel<<<E, 512, 0, s>>>(ids, Tk, El, my_rank, cnt_ptrs, pair_rank);
+  if (world > 512) return cudaErrorInvalidValue;
+  moe_count_kernel<<<E, 512, 0, s>>>(ids, Tk, E, world, my_rank, cnt_ptrs, pair_rank);
   return cudaGetLastError();
 }
 
-// Owner-side layout from the count matrix: segment start of each local expert (padded to 128 rows), the expert of
-// every 128-row block, and the row offset of each source inside each expert segment. cnt: [world][El].
-__global__ void moe_owner_layout_kernel(const int* __restrict__ cnt, int world, int El, int max_blocks,
-                                        int* __restrict__ src_off, int* __restrict__ m_block_expert,
-                                        int* __restrict__ num_blocks, int align) {
-  if (threadIdx.x != 0) return;
+// Layout of every owner's receive buffer from the full count matrix cnt [world(src)][E] (identical on every rank
+// after the count barrier).  Owner o holds experts [o*El, (o+1)*El); each expert's segment is padded to `align`
+// rows.  my_off[e]: the row of expert e's segment at its owner where this rank's rows start (sources in rank order).
+// For this rank's own experts: m_block_expert (expert of each 128-row block, -1 beyond) and num_blocks.
+// One thread per owner walks its El experts.
+__global__ void moe_layout_kernel(const int* __restrict__ cnt, int world, int E, int my_rank, int max_blocks,
+                                  int align, int* __restrict__ my_off, int* __restrict__ m_block_expert,
+                                  int* __restrict__ num_blocks) {
+  const int o = threadIdx.x;
+  if (o >= world) return;
+  const int El = E / world;
   int acc = 0, b = 0;
-  for (int e = 0; e < El; ++e) {
-    int n = 0;
+  for (int el = 0; el < El; ++el) {
+    const int e = o * El + el;
+    int n = 0, before = 0;
     for (int sr = 0; sr < world; ++sr) {
-      src_off[sr * El + e] = acc + n;
-      n += cnt[sr * El + e];
+      const int c = cnt[sr * E + e];
+      if (sr < my_rank) before += c;
+      n += c;
     }
+    my_off[e] = acc + before;
     const int nb = (n + align - 1) / align * (align / 128);   // 128-row blocks, segment padded to `align` rows
-    for (int j = 0; j < nb && b < max_blocks; ++j) m_block_expert[b++] = e;
+    if (o == my_rank)
+      for (int j = 0; j < nb && b < max_blocks; ++j) m_block_expert[b++] = el;
     acc += nb * 128;
   }
-  num_blocks[0] = b;
-  for (int j = b; j < max_blocks; ++j) m_block_expert[j] = -1;
+  if (o == my_rank) {
+    num_blocks[0] = b;
+    for (int j = b; j < max_blocks; ++j) m_block_expert[j] = -1;
+  }
 }
 
-cudaError_t moe_owner_layout(const int* cnt, int world, int El, int max_blocks, int* src_off, int* m_block_expert,
-                             int* num_blocks, cudaStream_t s, int align) {
-  if (align != 128 && align != 256) return cudaErrorInvalidValue;
-  moe_owner_layout_kernel<<<1, 32, 0, s>>>(cnt, world, El, max_blocks, src_off, m_block_expert, num_blocks, align);
+cudaError_t moe_layout(const int* cnt, int world, int E, int my_rank, int max_blocks, int align, int* my_off,
+                       int* m_block_expert, int* num_blocks, cudaStream_t s) {
+  if ((align != 128 && align != 256) || world > 1024 || E % world) return cudaErrorInvalidValue;
+  moe_layout_kernel<<<1, ((world + 31) / 32) * 32, 0, s>>>(cnt, world, E, my_rank, max_blocks, align, my_off,
+                                                           m_block_expert, num_blocks);
   return cudaGetLastError();
 }
 
 // Dispatch: one CTA (256 threads) per local token; the row is quantised once (1x128 UE8M0 blocks), then written to
-// each selected expert's owner at row  src_off_owner[my_rank][e_local] + pair_rank.  Destination rows are stored
-// in pos_out [T, k] (global row index inside the owner's buffer) for the combine.
-// recv_ptrs[r]: fp8 rows [cap, D]; sf_ptrs[r]: SF tiles of those rows (row blocks = cap/128); off_ptrs[r]: the
-// owner's src_off [world][El].
+// each selected expert's owner at row  my_off[e] + pair_rank.  Destination rows are stored in pos_out [T, k]
+// (row index inside the owner's buffer, -1 if it did not fit) for a pull combine; with rinfo_ptrs the owner also
+// learns where each received row goes back to: rinfo_owner[row] = (my_rank << 24) | (t * k + j), the slot of this
+// token's j-th expert in this rank's combine buffer (push combine from the owner's GEMM epilogue).
+// recv_ptrs[r]: fp8 rows [cap, D]; sf_ptrs[r]: SF tiles of those rows (row blocks = cap/128).
 __global__ void moe_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int D, const int* __restrict__ ids, int k,
                                     int El, int my_rank, const int* __restrict__ pair_rank,
                                     const uint64_t* __restrict__ recv_ptrs, const uint64_t* __restrict__ sf_ptrs,
-                                    const uint64_t* __restrict__ off_ptrs, int cap, int* __restrict__ pos_out,
-                                    int* __restrict__ status) {
+                                    const int* __restrict__ my_off, const uint64_t* __restrict__ rinfo_ptrs,
+                                    int cap, int* __restrict__ pos_out, int* __restrict__ status) {
   const int t = blockIdx.x;
   const int row_blocks = cap / 128;
   __shared__ int s_dst[16], s_owner[16];
   __shared__ uint32_t s_sf[64];            // UE8M0 scale of each 128-column block, four per word
   if (threadIdx.x < k) {
     const int e = ids[t * k + threadIdx.x];
-    const int owner = e / El, el = e % El;
-    const int base = reinterpret_cast<const int*>(off_ptrs[owner])[my_rank * El + el];
-    int row = base + pair_rank[t * k + threadIdx.x];
+    const int owner = e / El;
+    int row = my_off[e] + pair_rank[t * k + threadIdx.x];
     if (row >= cap) { if (status) atomicCAS(status, 0, kErrBadArg); row = -1; }
     s_dst[threadIdx.x] = row;
     s_owner[threadIdx.x] = owner;
     pos_out[t * k + threadIdx.x] = row;
+    if (rinfo_ptrs && row >= 0)
+      reinterpret_cast<int*>(rinfo_ptrs[owner])[row] = (my_rank << 24) | (t * k + threadIdx.x);
   }
   if (threadIdx.x < 64) s_sf[threadIdx.x] = 0x7f7f7f7fu;
   __syncthreads();
@@ -310,11 +325,67 @@ __global__ void moe_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int D, 
 
 cudaError_t moe_dispatch(const void* x, int T, int D, const int* ids, int k, int El, int my_rank,
                          const int* pair_rank, const uint64_t* recv_ptrs, const uint64_t* sf_ptrs,
-                         const uint64_t* off_ptrs, int cap, int* pos_out, int* status, cudaStream_t s) {
+                         const int* my_off, const uint64_t* rinfo_ptrs, int cap, int* pos_out, int* status,
+                         cudaStream_t s) {
   if (T == 0) return cudaSuccess;
-  if (D % 128 || D > 64 * 512 || k > 16 || cap % 128) return cudaErrorInvalidValue;
+  if (D % 128 || D > 64 * 512 || k > 16 || cap % 128 || (rinfo_ptrs && T * k > (1 << 24))) return cudaErrorInvalidValue;
   moe_dispatch_kernel<<<T, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), D, ids, k, El, my_rank, pair_rank,
-                                        recv_ptrs, sf_ptrs, off_ptrs, cap, pos_out, status);
+                                        recv_ptrs, sf_ptrs, my_off, rinfo_ptrs, cap, pos_out, status);
+  return cudaGetLastError();
+}
+
+// Push combine, home side: the owners' expert GEMMs stored every routed row into this rank's slots [T*k, D];
+// out[t] = add[t] + sum_j w[t,j] * slots[t*k + j] over the slots that were dispatched (pos >= 0).  Local reads only.
+template <int KMAX>
+__global__ void moe_combine_slots_kernel(const __nv_bfloat16* __restrict__ slots, int D, const int* __restrict__ pos,
+                                         const float* __restrict__ w, int k, const __nv_bfloat16* __restrict__ add,
+                                         __nv_bfloat16* __restrict__ out) {
+  const int t = blockIdx.x;
+  __shared__ float s_w[KMAX];
+  if (threadIdx.x < KMAX) {
+    const int j = threadIdx.x;
+    s_w[j] = (j < k && pos[t * k + j] >= 0) ? w[t * k + j] : 0.f;
+  }
+  __syncthreads();
+  const uint4* src = reinterpret_cast<const uint4*>(slots + size_t(t) * k * D);
+  for (int c = threadIdx.x; c < D / 8; c += blockDim.x) {
+    float acc[8];
+    if (add) {
+      const uint4 a = *reinterpret_cast<const uint4*>(add + size_t(t) * D + 8 * c);
+      acc[0] = bf16_lo(a.x); acc[1] = bf16_hi(a.x); acc[2] = bf16_lo(a.y); acc[3] = bf16_hi(a.y);
+      acc[4] = bf16_lo(a.z); acc[5] = bf16_hi(a.z); acc[6] = bf16_lo(a.w); acc[7] = bf16_hi(a.w);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < KMAX; ++j) {
+      if (j >= k) break;
+      const float wv = s_w[j];
+      if (wv == 0.f) continue;
+      const uint4 v = src[size_t(j) * (D / 8) + c];
+      acc[0] += wv * bf16_lo(v.x); acc[1] += wv * bf16_hi(v.x); acc[2] += wv * bf16_lo(v.y);
+      acc[3] += wv * bf16_hi(v.y); acc[4] += wv * bf16_lo(v.z); acc[5] += wv * bf16_hi(v.z);
+      acc[6] += wv * bf16_lo(v.w); acc[7] += wv * bf16_hi(v.w);
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]); o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]); o.w = pack_bf16x2(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(out + size_t(t) * D + 8 * c) = o;
+  }
+}
+
+cudaError_t moe_combine_slots(const void* slots, int T, int D, const int* pos, const float* w, int k, const void* add,
+                              void* out, cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  if (D % 8 || k > 16) return cudaErrorInvalidValue;
+  const auto* sl = reinterpret_cast<const __nv_bfloat16*>(slots);
+  const auto* a = reinterpret_cast<const __nv_bfloat16*>(add);
+  auto* o = reinterpret_cast<__nv_bfloat16*>(out);
+  if (k <= 8)
+    moe_combine_slots_kernel<8><<<T, 128, 0, s>>>(sl, D, pos, w, k, a, o);
+  else
+    moe_combine_slots_kernel<16><<<T, 128, 0, s>>>(sl, D, pos, w, k, a, o);
   return cudaGetLastError();
 }
 

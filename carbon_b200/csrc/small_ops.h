@@ -80,6 +80,9 @@ cudaError_t indexer_decode_logits(const void* q, const float* w, const void* kc,
                                   cudaStream_t s);
 cudaError_t topk_index(const float* logits, const int* key_slots, const int* n_keys, int T, int Lmax, int k,
                        int* out, cudaStream_t s);
+// general form: logits row stride ldo, slot row stride (0 = one shared slot list), n_keys or causal row0 + t + 1
+cudaError_t topk_slots(const float* logits, int ldo, const int* key_slots, int slot_stride, const int* n_keys,
+                       int row0, int T, int Lmax, int k, int* out, cudaStream_t s);
 
 // tcgen05 absorbed-MLA sparse attention over the latent cache (attn_decode.cu)
 // sink (optional, [H] fp32): per-head attention-sink logit; D: row width, 576 (MLA: 512 latent + 64 RoPE key) or

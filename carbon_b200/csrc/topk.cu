@@ -127,19 +127,23 @@ __global__ void topk_mask_kernel(const float* __restrict__ logits, int ldo, int 
 // ---------------------------------------------------------------------------------------------------------------
 // Decode-side DSA top-k (the logits come from the tcgen05 kernel in indexer_decode.cu).
 // ---------------------------------------------------------------------------------------------------------------
-// Top-k slot indices of each row (keys in key order, -1 padded): logits [T, Lmax], key_slots [T, Lmax].
-// Same radix select and lower-index tie rule as topk_mask_kernel; invalid keys carry -inf logits.
-__global__ void topk_index_kernel(const float* __restrict__ logits, const int* __restrict__ key_slots,
-                                  const int* __restrict__ n_keys, int Lmax, int k, int* __restrict__ out) {
+// Top-k slot indices of each row (keys in key order, -1 padded).  Row t's logits are logits[t * ldo + j] for its
+// candidate keys j < n_t; slot of key j: slots[t * slot_stride + j] (slot_stride 0: one slot list shared by every
+// row, e.g. the keys of one prefill sequence).  n_t = min(n_keys[t], Lmax), or with n_keys == nullptr the causal
+// count row0 + t + 1 (row t of a sequence block starting at position row0).  Same radix select and lower-index tie
+// rule as topk_mask_kernel; invalid keys carry -inf logits.
+__global__ void topk_index_kernel(const float* __restrict__ logits, int ldo, const int* __restrict__ key_slots,
+                                  int slot_stride, const int* __restrict__ n_keys, int row0, int Lmax, int k,
+                                  int* __restrict__ out) {
   extern __shared__ uint32_t vals[];
   __shared__ int hist[256];
   __shared__ int sw[32];
   __shared__ uint32_t s_prefix;
   __shared__ int s_remaining;
   const int t = blockIdx.x;
-  const int n = min(n_keys[t], Lmax);
-  const float* row = logits + size_t(t) * Lmax;
-  const int* slots = key_slots + size_t(t) * Lmax;
+  const int n = n_keys ? min(n_keys[t], Lmax) : min(row0 + t + 1, Lmax);
+  const float* row = logits + size_t(t) * ldo;
+  const int* slots = key_slots + size_t(t) * slot_stride;
   int* o = out + size_t(t) * k;
   if (n <= k) {
     for (int j = threadIdx.x; j < k; j += blockDim.x) o[j] = j < n ? slots[j] : -1;
@@ -189,8 +193,16 @@ __global__ void topk_index_kernel(const float* __restrict__ logits, const int* _
   }
 }
 
+cudaError_t topk_slots(const float* logits, int ldo, const int* key_slots, int slot_stride, const int* n_keys,
+                       int row0, int T, int Lmax, int k, int* out, cudaStream_t s);
+
 cudaError_t topk_index(const float* logits, const int* key_slots, const int* n_keys, int T, int Lmax, int k,
                        int* out, cudaStream_t s) {
+  return topk_slots(logits, Lmax, key_slots, Lmax, n_keys, 0, T, Lmax, k, out, s);
+}
+
+cudaError_t topk_slots(const float* logits, int ldo, const int* key_slots, int slot_stride, const int* n_keys,
+                       int row0, int T, int Lmax, int k, int* out, cudaStream_t s) {
   if (T == 0) return cudaSuccess;
   const size_t smem = size_t(Lmax) * 4;
   if (smem > 200 * 1024) return cudaErrorInvalidValue;
@@ -198,7 +210,7 @@ cudaError_t topk_index(const float* logits, const int* key_slots, const int* n_k
     cudaError_t e = smem_optin(topk_index_kernel, int(200 * 1024));
     if (e != cudaSuccess) return e;
   }
-  topk_index_kernel<<<T, 512, smem, s>>>(logits, key_slots, n_keys, Lmax, k, out);
+  topk_index_kernel<<<T, 512, smem, s>>>(logits, ldo, key_slots, slot_stride, n_keys, row0, Lmax, k, out);
   return cudaGetLastError();
 }
 

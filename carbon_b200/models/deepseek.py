@@ -470,7 +470,8 @@ class DeepseekModel:
             # prefill core (k / v of every token from wkv_b)
             with region("tp.gather"):
                 q_lat = pc.gather_rows(q_lat_a)
-                latent = pc.gather_rows(latent_l) if fb.is_prefill and cfg.attn_kind == "mla" else None
+                dense_prefill = fb.is_prefill and cfg.attn_kind == "mla" and not self._sparse_prefill(i, fb)
+                latent = pc.gather_rows(latent_l) if dense_prefill else None
             latent_c = latent_l
             idx_k = idx_l[1] if idx_l is not None else None
             out_loc = fb.out_loc[lo:hi]
@@ -504,6 +505,8 @@ class DeepseekModel:
         tok_major = False        # o holds this rank's tokens with every head (else: every token, this rank's heads)
         if cfg.attn_kind == "latent_mqa":
             o, tok_major = self._attn_latent(i, q, fb, cache, idx_l, dp)
+        elif fb.is_prefill and self._sparse_prefill(i, fb):
+            o, tok_major = self._attn_prefill_sparse(i, q, fb, cache, idx_l, dp)
         elif fb.is_prefill:
             o = self._attn_prefill(i, q, latent, fb, idx_l, cache, dp)
         else:
@@ -673,7 +676,35 @@ class DeepseekModel:
             C.rope_(o, r - dr, dr, self.cos_sin, fb.pos[lo:hi] if tok_major else pos_q, inverse=True)
         return o, tok_major
 
-    def _attn_decode(self, i, q, fb, cache, idx_l, dp: bool = False):
+    def _sparse_prefill(self, i, fb) -> bool:
+        """MLA prefill of this layer as absorbed sparse attention: the batch holds a sequence longer than
+        cfg.sparse_prefill_min and the layer has a DSA selection."""
+        cfg = self.cfg
+        if cfg.sparse_prefill_min <= 0 or cfg.attn_kind != "mla" or cfg.index_source(i) is None:
+            return False
+        cu = fb.cu_seqlens
+        return max(b - a for a, b in zip(cu[:-1], cu[1:])) > cfg.sparse_prefill_min
+
+    def _attn_prefill_sparse(self, i, q, fb, cache, idx_l, dp: bool = False):
+        """Long-prompt MLA prefill: every query attends to the cached latent rows of its DSA top-k keys through the
+        absorbed sparse kernel (the decode core), token-parallel; the new rows were written to the cache above."""
+        cfg, pc = self.cfg, self.pctx
+        lo, hi = pc.local
+        src = cfg.index_source(i)
+        if src == i:
+            with region("attn.indexer_topk"):
+                qi, ki, wi = idx_l
+                cu_l = [c - lo for c in fb.cu_seqlens if lo <= c <= hi]
+                sel = A.indexer_prefill_slots(qi, ki, wi, cu_l if len(cu_l) > 1 else [0, 0], cfg.index_topk,
+                                              fb.out_loc[lo:hi], fp8=cfg.index_fp8 and ki.shape[-1] % 128 == 0)
+            self._dsa[i] = sel
+        else:
+            sel = self._dsa[src]                    # selection shared with the index-source layer
+        return self._attn_decode(i, q, fb, cache, idx_l, dp, sel=sel)
+
+    def _attn_decode(self, i, q, fb, cache, idx_l, dp: bool = False, sel=None):
+        """Absorbed attention over cached latent rows (decode, verify, chunked prefill; and long prompts with
+        ``sel``: the DSA selection of this rank's queries as cache slots)."""
         cfg, L, pc = self.cfg, self.layers[i], self.pctx
         T, Hl = q.shape[0], self.H_local
         dn, r = cfg.qk_nope_head_dim, cfg.kv_lora_rank
@@ -686,9 +717,12 @@ class DeepseekModel:
         # only its own tokens' rows, for every head.
         swap = not dp and pc.world > 1 and hasattr(pc, "heads_to_tokens")
         local = dp or swap
-        idx = fb.key_slots[lo:hi] if local else fb.key_slots
         src = cfg.index_source(i)
-        if src is not None and int(fb.key_slots.shape[1]) > cfg.index_topk:
+        if sel is not None:
+            idx = sel if local or pc.world == 1 else pc.gather_rows(sel)
+        else:
+            idx = fb.key_slots[lo:hi] if local else fb.key_slots
+        if sel is None and src is not None and int(fb.key_slots.shape[1]) > cfg.index_topk:
             if src == i:
                 with region("attn.indexer_topk"):
                     qi, _, wi = idx_l

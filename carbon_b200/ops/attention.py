@@ -185,6 +185,48 @@ def sparse_mla(q: torch.Tensor, kv: torch.Tensor, idx: torch.Tensor, scale: floa
     return out
 
 
+def indexer_prefill_slots(q: torch.Tensor, k: torch.Tensor, w: torch.Tensor, cu_seqlens: List[int], topk: int,
+                          slots: torch.Tensor, fp8: bool = False) -> torch.Tensor:
+    """DSA selection of a prefill batch as cache slots (the sparse-prefill form of ``indexer_prefill_mask``): for
+    every query, the slots of its top-k causal keys, in key order, -1 padded; all causal keys when a query has at
+    most topk.  q [T, Hi, Di], k [T, Di], w [T, Hi]; slots [T] the cache slot of every token of the batch (the
+    sequences are contiguous runs of it).  Returns [T, topk] int32."""
+    T = cu_seqlens[-1]
+    out = torch.full((T, topk), -1, dtype=torch.int32, device=q.device)
+    if q.is_cuda:
+        if q.shape[1] % 16:
+            raise ValueError("the indexer kernel needs a multiple of 16 indexer heads")
+        e = ext()
+        for a, b in zip(cu_seqlens[:-1], cu_seqlens[1:]):
+            n = b - a
+            if n == 0:
+                continue
+            ldo = (n + 3) // 4 * 4
+            logits = torch.empty(n, ldo, dtype=torch.float32, device=q.device)
+            if n > topk and fp8:
+                from .quant import quant_act
+
+                kq, ksf = quant_act(k[a:b].contiguous())
+                qq, qsf = quant_act(q[a:b].reshape(n * q.shape[1], q.shape[2]).contiguous())
+                e.indexer_logits_fp8(kq, ksf, qq, qsf, q.shape[1], w[a:b].float().contiguous(), logits, True)
+            elif n > topk:
+                e.indexer_logits(k[a:b].contiguous(), q[a:b].contiguous(), w[a:b].float().contiguous(), logits, True)
+            e.topk_causal_slots(logits, slots[a:b].to(torch.int32).contiguous(), 0, out[a:b])
+        return out
+    if fp8:
+        q, k = R.fake_quant_fp8_rows(q), R.fake_quant_fp8_rows(k)
+    for a, b in zip(cu_seqlens[:-1], cu_seqlens[1:]):
+        n = b - a
+        if n == 0:
+            continue
+        pos = torch.arange(n)
+        m = R.topk_mask(R.indexer_logits(q[a:b], k[a:b], w[a:b]), pos, pos, topk)     # [n, n] bool
+        for i in range(n):
+            sel = torch.nonzero(m[i], as_tuple=False).flatten()
+            out[a + i, : sel.numel()] = slots[a:b][sel].to(torch.int32)
+    return out
+
+
 def indexer_topk(q: torch.Tensor, w: torch.Tensor, kcache: torch.Tensor, key_slots: torch.Tensor,
                  n_keys: torch.Tensor, topk: int) -> torch.Tensor:
     """For each query t: keys are ``key_slots[t, :n_keys[t]]`` (slots of ``kcache``), in causal order.

@@ -98,7 +98,7 @@ class FusedCtx(DistCtx):
         into column block `rank` of its buffer, one barrier."""
         T, Hl, W = x.shape
         cnt = self.counts()
-        buf = self._gbuf("h2t", (self.world * Hl, W), x.dtype, max(cnt))
+        buf = self._gbuf(f"h2t:{x.dtype}:{Hl}x{W}", (self.world * Hl, W), x.dtype, max(cnt))
         ext().p2p_a2a_heads(x.contiguous(), self._bounds_tensor(), self.rank, buf.peers, Hl * W * x.element_size(), 0,
                             max(cnt))
         self.barrier()
@@ -109,7 +109,7 @@ class FusedCtx(DistCtx):
         n, HW, W = y.shape
         Hl = HW // self.world
         T = self.bounds[-1] - self.bounds[0]
-        buf = self._gbuf("t2h", (Hl, W), y.dtype, T)
+        buf = self._gbuf(f"t2h:{y.dtype}:{Hl}x{W}", (Hl, W), y.dtype, T)
         ext().p2p_a2a_heads(y.contiguous(), self._bounds_tensor(), self.rank, buf.peers, Hl * W * y.element_size(), 1,
                             n)
         self.barrier()
@@ -180,62 +180,74 @@ class FusedCtx(DistCtx):
         ext().embed_peer(b.peers, per, ids, X, sumsq)
         return X, sumsq
 
-    def _moe_bufs(self, model, T_l: int, chunk: int = 0):
-        """Heap buffers of one MoE chunk: set 0 holds a whole call (max_local tokens), set 1 the second half of a
-        two-chunk call."""
+    def _moe_bufs(self, model, chunk: int, align: int, total_rows: int = 0):
+        """Heap buffers of one MoE chunk for one segment alignment: set 0 holds a whole call (max_local tokens), set
+        1 the second half of a two-chunk call.  256-aligned calls (prefill-sized) push the expert outputs to the
+        tokens' home ranks (`slots`); 128-aligned calls (decode-sized: fewer than 384 routed rows per expert over
+        all ranks) keep them in `y` for the homes to pull."""
         cfg = model.cfg
-        D, El, k = cfg.hidden_size, model.E_local, cfg.n_activated_experts
-        from ..ops.core import moe_align
-
-        # expert segments of the owner's buffer are padded to 256 rows (CTA-pair GEMM tiles) when experts average
-        # enough rows; the choice depends only on static sizes, so every rank makes the same one
-        align = moe_align(self.max_local * k * self.world, El * self.world)
+        D, El, k, E = cfg.hidden_size, model.E_local, cfg.n_activated_experts, cfg.n_routed_experts
         tokens = self.max_local if chunk == 0 else (self.max_local + 1) // 2
-        cap = int(tokens * k * self.moe_capacity) + El * align
-        cap = (cap + 255) // 256 * 256
+        rows = int(tokens * k * self.moe_capacity)
+        if align == 128:
+            # an owner receives at most the call's routed rows over all ranks (below 384 per expert at this
+            # alignment): size classes of powers of two, so decode-sized calls get small buffers
+            rows = min(rows, 1 << max(10, (max(total_rows, 1) - 1).bit_length()))
+        cap = (rows + El * align + 255) // 256 * 256
+        key = (chunk, align, cap)
         if self._moe is None:
-            self._moe = [None, None]
-        if self._moe[chunk] is None or self._moe[chunk]["align"] != align:
+            self._moe = {}
+        if key not in self._moe:
             h = self.heap
-            self._moe[chunk] = {
-                "cnt": h.alloc((self.world, El), torch.int32),
-                "off": h.alloc((self.world, El), torch.int32),
+            push = align == 256
+            self._moe[key] = {
+                "cnt": h.alloc((self.world, E), torch.int32),
+                "off": torch.empty(E, dtype=torch.int32, device=self.device),
                 "recv": h.alloc((cap, D), torch.float8_e4m3fn),
                 "sf": h.alloc((sf_words(cap, D),), torch.int32),
-                "y": h.alloc((cap, D), torch.bfloat16),
+                "rinfo": h.alloc((cap,), torch.int32),
+                "slots": h.alloc((tokens * k, D), torch.bfloat16) if push else None,
+                "y": None if push else h.alloc((cap, D), torch.bfloat16),
                 "cap": cap,
                 "mbe": torch.empty(cap // 128, dtype=torch.int32, device=self.device),
                 "nb": torch.empty(1, dtype=torch.int32, device=self.device),
                 "align": align,
+                "push": push,
             }
-        return self._moe[chunk]
+        return self._moe[key]
 
     # a call is split in two pipelined chunks once the whole batch has at least this many tokens per rank
     CHUNK_MIN_TOKENS_PER_RANK = 2048
 
     def moe(self, model, L, h, w, ids, shared, hq=None):
-        """EP MoE over NVLink.  Prefill-sized calls run as two token chunks on a communication stream and the
-        compute stream: chunk 1's dispatch overlaps chunk 0's expert GEMMs, chunk 0's combine overlaps chunk 1's.
-        Every cross-rank barrier is issued on the communication stream, in the same order on every rank."""
+        """EP MoE over NVLink.  Per chunk: counts to every rank -> barrier -> local layout + quantise and P2P row
+        stores into the owners' expert-sorted buffers -> barrier -> owner's grouped GEMMs, whose down-projection
+        epilogue stores each output row straight into its token's home-rank slot (prefill-sized calls) -> barrier ->
+        local weighted top-k sum.  Decode-sized calls keep the outputs on the owner and the homes pull them.
+        Prefill-sized calls run as two token chunks on a communication stream and the compute stream: chunk 1's
+        dispatch overlaps chunk 0's expert GEMMs, chunk 0's combine overlaps chunk 1's.  Every cross-rank barrier
+        is issued on the communication stream, in the same order on every rank."""
         cfg = model.cfg
         T, k = ids.shape
         ids = ids.to(torch.int32).contiguous()
         wf = w.float().contiguous()
         from ..models.deepseek import resolve
+        from ..ops.core import moe_align
         from ..utils.trace import region
 
         total = self.bounds[-1] - self.bounds[0] if self.bounds is not None else T
+        # segment alignment from the call's routed rows over all ranks (the same number on every rank)
+        align = moe_align(total * k, cfg.n_routed_experts)
+        gmode = 1 if align == 256 else (2 if total * k <= 32 * cfg.n_routed_experts else 0)
         chunked = total >= self.CHUNK_MIN_TOKENS_PER_RANK * self.world and self.device.type == "cuda"
         out = torch.empty(T, cfg.hidden_size, dtype=torch.bfloat16, device=h.device)
         if not chunked:
-            m = self._moe_bufs(model, T, 0)
+            m = self._moe_bufs(model, 0, align, total * k)
             with region("moe.dispatch"):
                 pos = self._moe_dispatch(model, m, h, ids)
-            self._moe_gemms(model, L, m)
+            self._moe_gemms(model, L, m, gmode)
             with region("moe.combine"):
-                self.barrier()
-                ext().moe_combine_pull(m["y"].peers, ids, pos, wf, model.E_local, resolve(shared), out)
-                self.barrier()     # peers may not reuse `y` until every rank has pulled its rows
+                self._moe_combine(model, m, ids, pos, wf, resolve(shared), out)
             return out
         main = torch.cuda.current_stream()
         if getattr(self, "_comm", None) is None:
@@ -243,7 +255,7 @@ class FusedCtx(DistCtx):
         cs = self._comm
         half = (T + 1) // 2
         spans = [(0, half), (half, T)]
-        bufs = [self._moe_bufs(model, T, c) for c in range(2)]
+        bufs = [self._moe_bufs(model, c, align, total * k) for c in range(2)]
         ev_disp = [torch.cuda.Event() for _ in range(2)]
         ev_gemm = [torch.cuda.Event() for _ in range(2)]
         poss = [None, None]
@@ -256,51 +268,67 @@ class FusedCtx(DistCtx):
                 ev_disp[c].record(cs)
         for c in range(2):
             main.wait_event(ev_disp[c])
-            self._moe_gemms(model, L, bufs[c])
+            self._moe_gemms(model, L, bufs[c], gmode)
             ev_gemm[c].record(main)
         with torch.cuda.stream(cs), region("moe.combine"):
             sh = resolve(shared)
             for c, (a, b) in enumerate(spans):
                 cs.wait_event(ev_gemm[c])
-                self.barrier()
-                if b > a:
-                    ext().moe_combine_pull(bufs[c]["y"].peers, ids[a:b], poss[c], wf[a:b], model.E_local,
-                                           sh[a:b] if sh is not None else None, out[a:b])
-            self.barrier()         # peers may not reuse `y` until every rank has pulled its rows
+                self._moe_combine(model, bufs[c], ids[a:b], poss[c], wf[a:b], sh[a:b] if sh is not None else None,
+                                  out[a:b])
         main.wait_stream(cs)
         return out
 
     def _moe_dispatch(self, model, m, h, ids):
-        """Count -> owner layout -> quantise + P2P row stores into the owners' expert-sorted buffers."""
+        """Counts -> barrier -> layout -> quantise + P2P row stores (and the rows' way back) -> barrier."""
         e = ext()
         cfg = model.cfg
         T, k = ids.shape
         El, E = model.E_local, cfg.n_routed_experts
+        # rows no source fills this call stay -1: the GEMM epilogues skip them.  Peers write rinfo only after the
+        # next barrier, and this rank's last read of it (its previous call's GEMMs) precedes this point.
+        m["rinfo"].local.fill_(-1)
         pair_rank = torch.empty(max(T * k, 1), dtype=torch.int32, device=self.device)
         e.moe_count(ids.reshape(-1), E, self.rank, m["cnt"].peers, pair_rank)
         self.barrier()
-        e.moe_owner_layout(m["cnt"].local, self.world, El, m["off"].local, m["mbe"], m["nb"], m["align"])
-        self.barrier()
+        e.moe_layout(m["cnt"].local, self.world, self.rank, m["off"], m["mbe"], m["nb"], m["align"])
         pos = torch.empty(T, k, dtype=torch.int32, device=self.device)
         if T > 0:
-            e.moe_dispatch(h.contiguous(), ids, El, self.rank, pair_rank, m["recv"].peers, m["sf"].peers,
-                           m["off"].peers, m["cap"], pos, self.status)
+            e.moe_dispatch(h.contiguous(), ids, El, self.rank, pair_rank, m["recv"].peers, m["sf"].peers, m["off"],
+                           m["rinfo"].peers, m["cap"], pos, self.status)
         self.barrier()
         return pos
 
-    def _moe_gemms(self, model, L, m):
-        """Owner side: grouped GEMMs over the expert-sorted received rows, in place in the heap."""
+    def _moe_gemms(self, model, L, m, gmode: int):
+        """Owner side: grouped GEMMs over the expert-sorted received rows, in place in the heap.  Push mode: the
+        down projection's epilogue stores every row into its home rank's combine slot over NVLink."""
         from ..utils.trace import region
 
         cfg = model.cfg
         I2 = 2 * cfg.moe_intermediate
-        mode = int(m["align"] == 256)
+        rv = m["rinfo"].local
         with region("moe.gemm_up"):
             act, act_sf = fp8_gemm_swiglu(m["recv"].local, m["sf"].local, L.e_w13, cfg.swiglu_limit, m["mbe"],
-                                          m["nb"], I2, pair=mode)
+                                          m["nb"], I2, pair=gmode, row_valid=rv if gmode == 2 else None)
         with region("moe.gemm_down"):
-            fp8_gemm(act, act_sf, L.e_w2, out=m["y"].local, m_block_expert=m["mbe"], num_m_blocks=m["nb"],
-                     n_per_group=cfg.hidden_size, pair=mode)
+            if m["push"]:
+                ext().gemm_fp8_push(act, act_sf, L.e_w2.q, L.e_w2.sf, m["mbe"], m["nb"], cfg.hidden_size, rv,
+                                    m["slots"].peers, self.status)
+            else:
+                fp8_gemm(act, act_sf, L.e_w2, out=m["y"].local, m_block_expert=m["mbe"], num_m_blocks=m["nb"],
+                         n_per_group=cfg.hidden_size, pair=gmode, row_valid=rv if gmode == 2 else None)
+
+    def _moe_combine(self, model, m, ids, pos, wf, shared, out):
+        """Home side.  Push mode: one barrier (every owner's stores into this rank's slots are done), then a local
+        weighted sum.  Pull mode: barrier, P2P loads of the outputs from the owners, barrier (owners may not reuse
+        `y` before every home has read it)."""
+        self.barrier()
+        if m["push"]:
+            ext().moe_combine_slots(m["slots"].local, pos, wf, shared, out)
+            return
+        if ids.shape[0] > 0:
+            ext().moe_combine_pull(m["y"].peers, ids, pos, wf, model.E_local, shared, out)
+        self.barrier()
 
     def lm_head(self, model, y: torch.Tensor) -> torch.Tensor:
         part = model.head_w(y, out_dtype=torch.float32)                     # [n, V/world]

@@ -1,6 +1,6 @@
 """Small, self-contained kernel cases for profiler captures (one launch of one kernel each, a few GB at most).
 
-    python -m carbon_b200.profile_cases gemm|grouped|moe_decode|attn|decode|indexer
+    python -m carbon_b200.profile_cases gemm|grouped|moe_decode|attn|decode|indexer|indexer_decode|ep_moe|oproj_a2a
 
 Each case sets up inputs larger than L2 where it can, runs its kernel twice (warm-up + the launch to capture) and
 exits 0, so that ``ncu -k regex:<kernel> -s 1 -c 1`` captures exactly one warm launch.
@@ -88,8 +88,70 @@ def indexer():
         indexer_prefill_mask(q, k, w, [0, 4096, 8192], 2048)
 
 
+def indexer_decode():
+    """Decode DSA indexer logits: 32 tokens x 4097 paged keys (64-token pages) x 64 heads (tcgen05 kernel)."""
+    from .ops._ext import ext
+
+    T, L, H, page = 32, 4097, 64, 64
+    S = T * (L // page + 2) * page
+    q = torch.randn(T, H, 128, device="cuda").to(torch.bfloat16)
+    w = torch.randn(T, H, device="cuda") * 0.01
+    kc = torch.randn(S, 128, device="cuda").to(torch.bfloat16)
+    pages = torch.randperm(S // page, device="cuda")[: T * (L // page + 1)].view(T, -1)
+    pos = torch.arange(L, device="cuda")
+    slots = (pages[:, pos // page] * page + pos % page).int().contiguous()
+    n = torch.full((T,), L, dtype=torch.int32, device="cuda")
+    out = torch.empty(T, L, device="cuda")
+    for _ in range(2):
+        ext().indexer_decode_logits(q, w, kc, slots, n, out)
+
+
+def _fused_one_rank():
+    """A one-rank FusedCtx (every peer pointer is this GPU's own heap): the fused collective kernels run alone."""
+    import os
+
+    import torch.distributed as dist
+
+    from .parallel.fused import FusedCtx
+
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29517")
+    if not dist.is_initialized():
+        dist.init_process_group("gloo", rank=0, world_size=1)
+    return FusedCtx(0, 1, heap_bytes=12 << 30, max_tokens=16384, max_seq=4096)
+
+
+def ep_moe():
+    """EP MoE layer through the fused path on one rank, 16384 tokens x top-8 of 64 experts (hidden 7168): count,
+    dispatch (quantise + row stores), grouped GEMMs with the push-combine epilogue, local combine."""
+    from .config import ModelConfig
+    from .models.deepseek import DeepseekModel
+    from .models.weights import WeightSource
+    from .ops import core as C
+
+    f = _fused_one_rank()
+    cfg = ModelConfig(n_layers=1, n_dense_layers=0, vocab_size=1024, n_routed_experts=64, index_n_heads=0)
+    m = DeepseekModel(cfg, WeightSource(cfg, seed=0), "cuda", pctx=f)
+    T = 16384
+    h = torch.randn(T, cfg.hidden_size, device="cuda").to(torch.bfloat16)
+    w, ids = C.router_topk(torch.randn(T, 64, device="cuda"), None, 8, "sigmoid", 2.5, True)
+    f.set_bounds([0, T])
+    for _ in range(2):
+        f.moe(m, m.layers[0], h, w, ids, None)
+
+
+def oproj_a2a():
+    """Head -> token all-to-all of 16384 tokens x 128 heads x 128 dims (bf16) on one rank (p2p_a2a_heads)."""
+    f = _fused_one_rank()
+    T = 16384
+    f.set_bounds([0, T])
+    o = torch.randn(T, 128, 128, device="cuda").to(torch.bfloat16)
+    for _ in range(2):
+        f.heads_to_tokens(o)
+
+
 if __name__ == "__main__":
     {"gemm": gemm, "grouped": grouped, "moe_decode": moe_decode, "attn": attn, "decode": decode,
-     "indexer": indexer}[sys.argv[1]]()
+     "indexer": indexer, "indexer_decode": indexer_decode, "ep_moe": ep_moe, "oproj_a2a": oproj_a2a}[sys.argv[1]]()
     torch.cuda.synchronize()
     print("ok", sys.argv[1])

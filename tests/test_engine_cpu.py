@@ -12,7 +12,7 @@ import pytest
 
 
 @pytest.mark.parametrize("variant", ["v3", "v3_plain", "v3_hf", "v41_features", "v4_latent", "v4_latent_nodsa", "v4_image",
-                                     "v4_late"])
+                                     "v4_late", "v3_sparse_prefill", "v41_sparse_prefill"])
 def test_tiny_engine_matches_oracle(variant):
     """v41_features: DSA selection computed by index-source layers 1 and 3 only (layer 0 dense, layer 2 reuses
     layer 1's selection) and per-head attention sinks.  v4_latent: the V4 attention layout (latent MQA with output
@@ -20,7 +20,9 @@ def test_tiny_engine_matches_oracle(variant):
     sqrt-softplus router, Engram on layer 1); v4_latent_nodsa: the same without the indexer (window-only attention);
     v4_image: image tokens (every 5th prompt token) rank experts with the image bias and skip the Engram update;
     v4_late: bounded late-layer replay (layer 2 runs only each prompt's last 24 tokens, window-only); v3_plain: no
-    hyper-connections (one residual stream, x + f(norm(x)), as in DeepSeek-V3 / V3.2 checkpoints)."""
+    hyper-connections (one residual stream, x + f(norm(x)), as in DeepSeek-V3 / V3.2 checkpoints); *_sparse_prefill:
+    the 64-token prompts run the long-prompt MLA prefill (absorbed sparse attention over each query's top-k cached
+    rows) instead of the dense masked kernel."""
     cfg = tiny_config()
     if variant == "v3_plain":
         cfg = cfg.replace(hc_mult=0, n_layers=3, n_dense_layers=1)
@@ -36,6 +38,10 @@ def test_tiny_engine_matches_oracle(variant):
         cfg = tiny_v4_config().replace(image_token_id=7)
     elif variant == "v4_late":
         cfg = tiny_v4_config().replace(n_layers=3, late_layer_start=2, late_replay=24)
+    elif variant == "v3_sparse_prefill":
+        cfg = cfg.replace(sparse_prefill_min=40)
+    elif variant == "v41_sparse_prefill":
+        cfg = cfg.replace(n_layers=4, index_sources=(1, 3), attn_sink=True, sparse_prefill_min=40)
     w = init_weights(cfg, seed=0)
     ref = RefModel(cfg, w)
     g = torch.Generator().manual_seed(1)
