@@ -24,16 +24,20 @@ namespace mla {
 constexpr int HM = 128;                // head rows per CTA (M)
 // A row is NA 64-dim atoms: NA = 9 for MLA (512 latent + 64 RoPE key), NA = 8 for latent MQA (one 512-dim head whose
 // last 64 dims carry RoPE).  The value is always the first DL = 512 dims of the row.
-constexpr int D = 576, DL = 512, DHALF = 256;
+constexpr int DL = 512, DHALF = 256;
 constexpr int KT = 32;                 // keys per tile (N of Q·Kᵀ, K of P·V)
-constexpr int STAGES = 2;
+constexpr int STAGES = 5;
+constexpr int NAC_MAX = 5;             // atoms one CTA of the pair owns (value half + the RoPE atom)
 constexpr int Q_ATOM = HM * 128;       // 16 KB: 128 rows x 64 dims
 constexpr int KV_ATOM = KT * 128;      // 4 KB: 32 rows x 64 dims
+constexpr int KV_STAGE = NAC_MAX * KV_ATOM;
+constexpr int X_BYTES = HM * KT * 4;   // one partial-score exchange buffer: 128 rows x 32 fp32
 // TMEM: O [128 x 256] fp32 at columns [0, 256); two S buffers of 64 columns at 256 and 320 (P overwrites the first
 // KT/2 columns of its S buffer as packed bf16 and is read there by the P·V MMA)
 constexpr int TM_O = 0, TM_S = 256, TM_S_STRIDE = 64;
+constexpr int SMEM = 1024 + NAC_MAX * Q_ATOM + STAGES * KV_STAGE + 2 * X_BYTES + 256;
 template <int NA>
-constexpr int smem_bytes() { return 1024 + NA * Q_ATOM + STAGES * NA * KV_ATOM + 256; }
+constexpr int smem_bytes() { return SMEM; }
 constexpr float kRescaleThresh = 8.0f;
 
 struct Params {
@@ -64,59 +68,76 @@ CB_DEVICE void tma_gather4(void* dst, const void* tmap, uint64_t* bar, int col, 
       : "memory");
 }
 
-// Pipeline (one CTA = one token, one value half, one key split):
-//   TMA   Q once; KV tile j into stage j % 2 after P·V(j-2) released it
+// Global atom index of local atom `la` in CTA `hh` of the pair: the CTA's value half (atoms 4hh .. 4hh+3) first,
+// then (MLA rows, CTA 0) the RoPE-key atom 8.
+CB_DEVICE int atom_of(int hh, int la) { return la < 4 ? hh * 4 + la : 8; }
+
+// One token's keys [split*chunk, ...) are handled by a cluster of two CTAs (blockIdx.y = cluster rank hh).  The row
+// of a cached key is split between them by 64-dim atoms: CTA hh gathers only its value half (and CTA 0 the RoPE
+// atom), so no byte of a key row is read twice, and a CTA keeps 5 tiles of 32 keys in flight.  Each CTA computes the
+// partial S over its atoms; the two partials are exchanged through distributed shared memory every tile, so both
+// CTAs hold the same S and the same softmax (addition is commutative: identical m, l and P), and each accumulates
+// P·V for its own value half.
+//   TMA   Q atoms once; the CTA's atoms of KV tile j into stage j % 5 after P·V(j-5) released it
 //   MMA   QK(0) QK(1) | PV(0) QK(2) | PV(1) QK(3) | ...   S(j) goes to buffer j % 2; PV(j) reads P(j) from the same
 //         columns and QK(j+2) overwrites them afterwards (tcgen05 MMAs of one thread execute in issue order)
-//   softmax (one head row per thread) of tile j+1 runs while PV(j) and QK(j+2) are on the tensor pipe; O is
-//         rescaled lazily, only when the running max grows by more than 2^8, after waiting for the previous PV.
+//   softmax (one head row per thread): partial S -> peer's exchange buffer, peer's partial + own = S, online
+//         softmax with lazy O rescale (only when the running max grows by more than 2^8), P over S in TMEM
 template <int NA>
 __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constant__ CUtensorMap tm_q,
                                                             const __grid_constant__ CUtensorMap tm_kv,
                                                             const Params p) {
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 1000
-  constexpr int Q_BYTES = NA * Q_ATOM, KV_BYTES = NA * KV_ATOM, D = 64 * NA;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
-  uint8_t* sKV = sQ + Q_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + STAGES * KV_BYTES);
+  uint8_t* sKV = sQ + NAC_MAX * Q_ATOM;
+  float* xbuf = reinterpret_cast<float*>(sKV + STAGES * KV_STAGE);   // [2][128][KT]: the PEER's partial S
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(xbuf) + 2 * X_BYTES);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;              // [STAGES]
   uint64_t* kv_empty = kv_full + STAGES;     // [STAGES]
   uint64_t* s_full = kv_empty + STAGES;      // [2]
   uint64_t* p_full = s_full + 2;             // [2]
   uint64_t* pv_done = p_full + 2;            // [2]: PV(j) completes phase j >> 1 of pv_done[j & 1]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
+  uint64_t* x_full = pv_done + 2;            // [2]: the peer wrote its partial of tile j into xbuf[j & 1]
+  uint64_t* x_empty = x_full + 2;            // [2]: the peer consumed this CTA's partial of tile j
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(x_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-  const int t = blockIdx.x, hh = blockIdx.y, split = blockIdx.z;
+  const int t = blockIdx.x, hh = int(cluster_ctarank()), split = blockIdx.z;
+  const uint32_t peer = uint32_t(hh ^ 1);
+  const int nac = (NA == 9 && hh == 0) ? 5 : 4;
+  const int kv_bytes = nac * KV_ATOM;
   const int k_begin = split * p.chunk;
   const int k_end = min(p.K, k_begin + p.chunk);
-  const int n_tiles = k_end > k_begin ? (k_end - k_begin + KT - 1) / KT : 0;
+  const int n_tiles = k_end > k_begin ? (k_end - k_begin + KT - 1) / KT : 0;   // the same in both CTAs
   const int* idx_t = p.idx + size_t(t) * p.K;
   const uint32_t warp = warp_id(), lane = lane_id();
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
     for (int i = 0; i < STAGES; ++i) { mbar_init(&kv_full[i], 1); mbar_init(&kv_empty[i], 1); }
-    for (int i = 0; i < 2; ++i) { mbar_init(&s_full[i], 1); mbar_init(&p_full[i], 128); mbar_init(&pv_done[i], 1); }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1); mbar_init(&p_full[i], 128); mbar_init(&pv_done[i], 1);
+      mbar_init(&x_full[i], 128); mbar_init(&x_empty[i], 128);
+    }
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 2) { tmem_alloc(tmem_slot, 512); tmem_relinquish(); }
   tc_fence_before();
-  __syncthreads();
+  cluster_sync();                            // both CTAs' barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   auto fail = [&](int code) { if (p.status) atomicCAS(p.status, 0, code); *abort_flag = 1; };
 
   if (warp == 0) {
-    // ---------------- TMA: Q once, then gathered KV rows ----------------
+    // ---------------- TMA: this CTA's Q atoms once, then its atoms of the gathered KV rows ----------------
     if (lane == 0 && n_tiles > 0) {
       tma_prefetch_desc(&tm_q); tma_prefetch_desc(&tm_kv);
-      mbar_arrive_expect_tx(q_full, Q_BYTES);
-      for (int a = 0; a < NA; ++a) tma_load_3d(sQ + a * Q_ATOM, &tm_q, q_full, a * 64, 0, t);
+      mbar_arrive_expect_tx(q_full, nac * Q_ATOM);
+      for (int la = 0; la < nac; ++la) tma_load_3d(sQ + la * Q_ATOM, &tm_q, q_full, atom_of(hh, la) * 64, 0, t);
     }
     for (int j = 0; j < n_tiles; ++j) {
       const int s = j % STAGES;
@@ -126,21 +147,20 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
       int ok = 1;
       if (lane == 0) {
         ok = mbar_wait(&kv_empty[s], ((j / STAGES) & 1) ^ 1) ? 1 : 0;
-        if (ok) mbar_arrive_expect_tx(&kv_full[s], KV_BYTES);
+        if (ok) mbar_arrive_expect_tx(&kv_full[s], kv_bytes);
         else fail(kErrTimeoutEmpty);
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok || *abort_flag) break;
-      int r[KT];
-#pragma unroll
-      for (int i = 0; i < KT; ++i) r[i] = __shfl_sync(0xffffffffu, slot, i);
-      if (lane < NA) {                                         // lane a issues the 8 gathers of 64-dim atom a
-        uint8_t* dst = sKV + s * KV_BYTES + lane * KV_ATOM;
-#pragma unroll
-        for (int g = 0; g < KT / 4; ++g)
-          tma_gather4(dst + g * 4 * 128, &tm_kv, &kv_full[s], lane * 64, r[4 * g], r[4 * g + 1], r[4 * g + 2],
-                      r[4 * g + 3]);
-      }
+      // lane (la, g): local atom la = lane / 8, row group g = lane % 8 (rows 4g..4g+3)
+      const int la = int(lane >> 3), g = int(lane & 7);
+      const int r0 = __shfl_sync(0xffffffffu, slot, 4 * g), r1 = __shfl_sync(0xffffffffu, slot, 4 * g + 1);
+      const int r2 = __shfl_sync(0xffffffffu, slot, 4 * g + 2), r3 = __shfl_sync(0xffffffffu, slot, 4 * g + 3);
+      if (la < 4)
+        tma_gather4(sKV + s * KV_STAGE + la * KV_ATOM + g * 4 * 128, &tm_kv, &kv_full[s], atom_of(hh, la) * 64, r0,
+                    r1, r2, r3);
+      if (nac == 5 && la == 0)                                 // the RoPE atom (CTA 0 of MLA rows)
+        tma_gather4(sKV + s * KV_STAGE + 4 * KV_ATOM + g * 4 * 128, &tm_kv, &kv_full[s], 8 * 64, r0, r1, r2, r3);
       __syncwarp();
     }
   } else if (warp == 1) {
@@ -154,11 +174,11 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
         const int s = j % STAGES, b = j & 1;
         if (!mbar_wait(&kv_full[s], (j / STAGES) & 1)) { fail(kErrTimeoutFull); return false; }
         tc_fence_after();
-#pragma unroll 4
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const int a = kk >> 2, off = (kk & 3) * 32;
-          mma_f16_ss(tmem + TM_S + b * TM_S_STRIDE, smem_desc_sw128(sQ + a * Q_ATOM + off),
-                     smem_desc_sw128(sKV + s * KV_BYTES + a * KV_ATOM + off), id_qk, kk > 0);
+        for (int la = 0; la < nac; ++la) {
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_f16_ss(tmem + TM_S + b * TM_S_STRIDE, smem_desc_sw128(sQ + la * Q_ATOM + kk * 32),
+                       smem_desc_sw128(sKV + s * KV_STAGE + la * KV_ATOM + kk * 32), id_qk, (la | kk) > 0);
         }
         mma_commit(&s_full[b]);
         return true;
@@ -170,7 +190,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
 #pragma unroll
         for (int k = 0; k < KT / 16; ++k)
           mma_f16_ts(tmem + TM_O, tmem + TM_S + b * TM_S_STRIDE + 8 * k,
-                     desc_mn_sw128(sKV + s * KV_BYTES + (hh * 4) * KV_ATOM + k * 16 * 128, KV_ATOM, 1024), id_pv,
+                     desc_mn_sw128(sKV + s * KV_STAGE + k * 16 * 128, KV_ATOM, 1024), id_pv,
                      (j > 0 || k > 0) ? 1u : 0u);
         mma_commit(&pv_done[b]);
         mma_commit(&kv_empty[s]);
@@ -184,7 +204,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
       }
     }
   } else if (warp >= 4) {
-    // ---------------- softmax / rescale / epilogue ----------------
+    // ---------------- partial-score exchange, softmax / rescale / epilogue ----------------
     const uint32_t q = warp & 3;
     const int row = q * 32 + lane;               // head
     const uint32_t t_lane = tmem + ((q * 32) << 16);
@@ -200,11 +220,29 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
       const int my_key = k_begin + j * KT + lane;
       const uint32_t vmask = __ballot_sync(0xffffffffu, my_key < k_end && __ldg(idx_t + my_key) >= 0);
       tmem_ld_wait();
+      // my partial -> the peer's exchange buffer b (once the peer has consumed what I wrote there two tiles ago)
+      if (!mbar_wait(&x_empty[b], ((j >> 1) & 1) ^ 1)) { fail(kErrTimeoutPeer); ok = false; break; }
+      const uint32_t xrow = mapa_shared(smem_u32(xbuf + (b * HM + row) * KT), peer);
+#pragma unroll
+      for (int c = 0; c < KT / 4; ++c) st_cluster_v4(xrow + 16 * c, r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
+      mbar_arrive_cluster_release(mapa_shared(smem_u32(&x_full[b]), peer));
+      // the peer's partial of this tile
+      if (!mbar_wait_cluster(&x_full[b], (j >> 1) & 1)) { fail(kErrTimeoutPeer); ok = false; break; }
+      const float4* xr = reinterpret_cast<const float4*>(xbuf + (b * HM + row) * KT);
       float sv[KT];
+#pragma unroll
+      for (int c = 0; c < KT / 4; ++c) {
+        const float4 v = xr[c];
+        sv[4 * c + 0] = __uint_as_float(r[4 * c + 0]) + v.x;
+        sv[4 * c + 1] = __uint_as_float(r[4 * c + 1]) + v.y;
+        sv[4 * c + 2] = __uint_as_float(r[4 * c + 2]) + v.z;
+        sv[4 * c + 3] = __uint_as_float(r[4 * c + 3]) + v.w;
+      }
+      mbar_arrive_cluster_release(mapa_shared(smem_u32(&x_empty[b]), peer));   // my buffer b is free again
       float mt = -INFINITY;
 #pragma unroll
       for (int i = 0; i < KT; ++i) {
-        sv[i] = ((vmask >> i) & 1u) ? __uint_as_float(r[i]) * p.scale_log2 : -INFINITY;
+        sv[i] = ((vmask >> i) & 1u) ? sv[i] * p.scale_log2 : -INFINITY;
         mt = fmaxf(mt, sv[i]);
       }
       const bool need = (j > 0) && (mt > m_used + kRescaleThresh);
@@ -293,6 +331,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
     }
   }
   __syncthreads();
+  cluster_sync();          // the peer no longer writes into this CTA's exchange buffers or arrives on its barriers
   if (warp == 2) { tc_fence_after(); tmem_dealloc(tmem, 512); }
 #endif
 }
@@ -381,10 +420,21 @@ cudaError_t sparse_mla(const void* q, int T, int H, const void* kv, int S, const
   p.out = reinterpret_cast<__nv_bfloat16*>(out);
   p.status = status;
   p.sink = sink;
-  if (D == 576)
-    sparse_mla_kernel<9><<<dim3(T, 2, n_splits), 256, smem_bytes<9>(), s>>>(tq, tkv, p);
-  else
-    sparse_mla_kernel<8><<<dim3(T, 2, n_splits), 256, smem_bytes<8>(), s>>>(tq, tkv, p);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1; attr[0].val.clusterDim.y = 2; attr[0].val.clusterDim.z = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(T, 2, n_splits);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = SMEM;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  {
+    cudaError_t e = D == 576 ? cudaLaunchKernelEx(&cfg, sparse_mla_kernel<9>, tq, tkv, p)
+                             : cudaLaunchKernelEx(&cfg, sparse_mla_kernel<8>, tq, tkv, p);
+    if (e != cudaSuccess) return e;
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || n_splits == 1) return e;
   mla_combine_kernel<<<dim3(T, H), 128, 0, s>>>(part_o, part_ml, n_splits, H, reinterpret_cast<__nv_bfloat16*>(out),

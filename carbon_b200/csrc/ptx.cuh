@@ -260,6 +260,38 @@ CB_DEVICE uint32_t mapa_shared(uint32_t cta_addr, uint32_t rank) {
 CB_DEVICE void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// Release-at-cluster-scope arrive on an mbarrier of a CTA of the cluster: this thread's earlier shared::cluster
+// stores are visible to a thread that observes the phase with an acquire.cluster wait.
+CB_DEVICE void mbar_arrive_cluster_release(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+CB_DEVICE bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, P;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded acquire.cluster wait (data written by the other CTA of the cluster before its release arrive).
+CB_DEVICE bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  uint32_t n = 0;
+  while (!mbar_try_wait_cluster(bar, parity)) {
+    if ((++n & 255u) == 0 && globaltimer() - t0 > kWaitLimitNs) return false;
+  }
+  return true;
+}
+// 16-byte store into the shared memory of a CTA of the cluster (address from mapa).
+CB_DEVICE void st_cluster_v4(uint32_t cluster_addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "r"(a), "r"(b), "r"(c),
+               "r"(d)
+               : "memory");
+}
 // TMA tile load into this CTA's shared memory whose completion is counted on an mbarrier of either CTA of the
 // pair (`bar_cluster_addr`, from mapa).  Plain unicast load.
 CB_DEVICE void tma_load_2d_pair(void* smem_dst, const void* tmap, uint32_t bar_cluster_addr, int c0, int c1) {

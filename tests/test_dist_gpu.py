@@ -59,7 +59,7 @@ def _run_forced(eng, prompts, steps=4):
     return hist
 
 
-def _worker(rank, world, port, comm, q, attn_dp=False, v4=False):
+def _worker(rank, world, port, comm, q, attn_dp=False, v4=False, owner=False):
     from datetime import timedelta
 
     from carbon_b200.engine.engine import Engine
@@ -78,15 +78,17 @@ def _worker(rank, world, port, comm, q, attn_dp=False, v4=False):
     try:
         cfg = _cfg_v4() if v4 else _cfg()
         w = init_weights(cfg, seed=0)
-        if comm == "fused":
-            pctx = FusedCtx(rank, world, heap_bytes=1 << 30, max_tokens=1024, max_seq=512, attn_dp=attn_dp)
+        if comm.startswith("fused"):
+            pctx = FusedCtx(rank, world, heap_bytes=1 << 30, max_tokens=1024, max_seq=512, attn_dp=attn_dp,
+                            oproj_a2a=comm != "fused-rs")
         else:
             pctx = DistCtx(rank, world, attn_dp=attn_dp)
-        eng = Engine(cfg, device=dev, source=WeightSource(cfg, state=w), num_pages=64, page_size=64, pctx=pctx)
+        eng = Engine(cfg, device=dev, source=WeightSource(cfg, state=w), num_pages=64, page_size=64, pctx=pctx,
+                     owner_kv=owner)
         hist = _run_forced(eng, _prompts(cfg))
         outs = []
         torch.cuda.synchronize()
-        status = pctx.check() if comm == "fused" else 0
+        status = pctx.check() if comm.startswith("fused") else 0
         q.put((rank, outs, [h.numpy().copy() for h in hist], status))
         ok = True
         dist.barrier()
@@ -99,9 +101,15 @@ def _worker(rank, world, port, comm, q, attn_dp=False, v4=False):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("comm,attn_dp,v4", [("fused", False, False), ("nccl", False, False), ("fused", True, False),
-                                             ("nccl", True, False), ("fused", False, True), ("fused", True, True)])
-def test_two_gpu_engine_matches_single_gpu(comm, attn_dp, v4):
+@pytest.mark.parametrize("comm,attn_dp,v4,owner", [
+    ("fused", False, False, False), ("nccl", False, False, False), ("fused", True, False, False),
+    ("nccl", True, False, False), ("fused", False, True, False), ("fused", True, True, False),
+    # owner-only KV (each request's KV on its home rank), TP with the all-to-all output projection and DP
+    ("fused", False, False, True), ("fused", True, False, True), ("fused", False, True, True),
+    ("nccl", False, False, True),
+    # TP attention with the row-parallel projection fused with the reduce-scatter (the earlier fused path)
+    ("fused-rs", False, False, False)])
+def test_two_gpu_engine_matches_single_gpu(comm, attn_dp, v4, owner):
     from carbon_b200.engine.engine import Engine
     from carbon_b200.models.weights import WeightSource
     from carbon_b200.ref.model import init_weights
@@ -115,7 +123,7 @@ def test_two_gpu_engine_matches_single_gpu(comm, attn_dp, v4):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, comm, q, attn_dp, v4)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, comm, q, attn_dp, v4, owner)) for r in range(2)]
     for p in procs:
         p.start()
     res = [q.get(timeout=420) for _ in range(2)]
