@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
   uint64_t* s_full = kv_empty + STAGES;      // [2]
   uint64_t* p_full = s_full + 2;             // [2]
   uint64_t* pv_done = p_full + 2;            // [2]: PV(j) completes phase j >> 1 of pv_done[j & 1]
-  uint64_t* x_full = pv_done + 2;            // [2]: the peer wrote its partial of tile j into xbuf[j & 1]
+  uint64_t* x_full = pv_done + 2;            // [2]: the peer's partial of tile j landed in xbuf[j & 1] (tx bytes)
   uint64_t* x_empty = x_full + 2;            // [2]: the peer consumed this CTA's partial of tile j
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(x_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -120,7 +120,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
     for (int i = 0; i < STAGES; ++i) { mbar_init(&kv_full[i], 1); mbar_init(&kv_empty[i], 1); }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1); mbar_init(&p_full[i], 128); mbar_init(&pv_done[i], 1);
-      mbar_init(&x_full[i], 128); mbar_init(&x_empty[i], 128);
+      mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], 128);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -210,24 +210,32 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
     const uint32_t t_lane = tmem + ((q * 32) << 16);
     float m_used = -INFINITY, l = 0.f;
     bool ok = true;
+    // validity of a tile's keys (one per lane): the slot of the next tile is loaded one tile ahead, so its global
+    // load latency stays off the per-tile chain
+    int next_slot = k_begin + lane < k_end ? __ldg(idx_t + k_begin + lane) : -1;
     for (int j = 0; j < n_tiles; ++j) {
       const int b = j & 1;
+      const int my_slot = next_slot;
+      const int nk = k_begin + (j + 1) * KT + lane;
+      next_slot = nk < k_end ? __ldg(idx_t + nk) : -1;
       if (!mbar_wait(&s_full[b], (j >> 1) & 1)) { fail(kErrTimeoutTmem); ok = false; break; }
       tc_fence_after();
       uint32_t r[KT];
       tmem_ld_32x32b_x32(t_lane + TM_S + b * TM_S_STRIDE, r);
-      // validity of the tile's keys (one per lane), as a bit mask shared by the warp
-      const int my_key = k_begin + j * KT + lane;
-      const uint32_t vmask = __ballot_sync(0xffffffffu, my_key < k_end && __ldg(idx_t + my_key) >= 0);
+      const uint32_t vmask = __ballot_sync(0xffffffffu, my_slot >= 0);
       tmem_ld_wait();
-      // my partial -> the peer's exchange buffer b (once the peer has consumed what I wrote there two tiles ago)
+      // arm this CTA's receive barrier for the peer's partial of tile j (its stores count down the bytes)
+      if (row == 0) mbar_arrive_expect_tx(&x_full[b], X_BYTES);
+      // my partial -> the peer's exchange buffer b (once the peer has consumed what I wrote there two tiles ago):
+      // asynchronous stores whose bytes complete the peer's x_full[b], no fence on this side
       if (!mbar_wait(&x_empty[b], ((j >> 1) & 1) ^ 1)) { fail(kErrTimeoutPeer); ok = false; break; }
       const uint32_t xrow = mapa_shared(smem_u32(xbuf + (b * HM + row) * KT), peer);
+      const uint32_t xbar = mapa_shared(smem_u32(&x_full[b]), peer);
 #pragma unroll
-      for (int c = 0; c < KT / 4; ++c) st_cluster_v4(xrow + 16 * c, r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
-      mbar_arrive_cluster_release(mapa_shared(smem_u32(&x_full[b]), peer));
+      for (int c = 0; c < KT / 4; ++c)
+        st_async_v4(xrow + 16 * c, r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3], xbar);
       // the peer's partial of this tile
-      if (!mbar_wait_cluster(&x_full[b], (j >> 1) & 1)) { fail(kErrTimeoutPeer); ok = false; break; }
+      if (!mbar_wait(&x_full[b], (j >> 1) & 1)) { fail(kErrTimeoutPeer); ok = false; break; }
       const float4* xr = reinterpret_cast<const float4*>(xbuf + (b * HM + row) * KT);
       float sv[KT];
 #pragma unroll
@@ -238,7 +246,6 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
         sv[4 * c + 2] = __uint_as_float(r[4 * c + 2]) + v.z;
         sv[4 * c + 3] = __uint_as_float(r[4 * c + 3]) + v.w;
       }
-      mbar_arrive_cluster_release(mapa_shared(smem_u32(&x_empty[b]), peer));   // my buffer b is free again
       float mt = -INFINITY;
 #pragma unroll
       for (int i = 0; i < KT; ++i) {
@@ -274,6 +281,8 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
         pk[i / 2] = pack_bf16x2(a0, a1);
       }
       tmem_st_32x32b_x16(t_lane + TM_S + b * TM_S_STRIDE, pk);   // P over the first KT/2 columns of S(j)
+      // my exchange buffer b is free again: P (issued above) is computed from its values, so their loads are done
+      mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&x_empty[b]), peer));
       l = l * alpha + (rs0 + rs1);
       m_used = m_new;
       tmem_st_wait();

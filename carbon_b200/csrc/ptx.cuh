@@ -286,6 +286,19 @@ CB_DEVICE bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
   }
   return true;
 }
+// Asynchronous 16-byte store into the shared memory of a CTA of the cluster whose completion is counted
+// (complete_tx, 16 bytes) on an mbarrier of that CTA: no fence on the sender; a thread that observes the barrier's
+// phase sees the data.
+CB_DEVICE void st_async_v4(uint32_t cluster_addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d,
+                           uint32_t cluster_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];"
+               ::"r"(cluster_addr), "r"(a), "r"(b), "r"(c), "r"(d), "r"(cluster_bar)
+               : "memory");
+}
+// Relaxed arrive on an mbarrier of a CTA of the cluster (a signal that orders nothing but itself).
+CB_DEVICE void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
 // 16-byte store into the shared memory of a CTA of the cluster (address from mapa).
 CB_DEVICE void st_cluster_v4(uint32_t cluster_addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(cluster_addr), "r"(a), "r"(b), "r"(c),
