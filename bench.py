@@ -208,7 +208,9 @@ def main():
 
     def phase(name):                      # progress on stderr: a stalled run shows where it stopped
         if rank == 0:
-            print(f"[bench] {time.time() - t_start:8.1f}s {name}", file=sys.stderr, flush=True)
+            mem = torch.cuda.max_memory_allocated(dev) / 2 ** 30
+            print(f"[bench] {time.time() - t_start:8.1f}s {name} (peak {mem:.1f} GiB allocated)", file=sys.stderr,
+                  flush=True)
 
     phase(f"engine ready (init {init_s:.1f}s)")
 

@@ -331,9 +331,13 @@ class DeepseekModel:
         if L.has_indexer:
             ix = a + "indexer."
             L.idx_wq = Lin(get(ix + "wq.weight"), dev, fp8=False)
-            L.idx_wk = Lin(get(ix + "wk.weight"), dev, fp8=False)
             L.idx_kn_w, L.idx_kn_b = get(ix + "k_norm.weight"), get(ix + "k_norm.bias")
-            L.idx_wp = Lin(get(ix + "weights_proj.weight"), dev, fp8=False)
+            if dev.type == "cpu":
+                L.idx_wk = Lin(get(ix + "wk.weight"), dev, fp8=False)
+                L.idx_wp = Lin(get(ix + "weights_proj.weight"), dev, fp8=False)
+            else:
+                # the key and head-weight projections read the same input: one GEMM, fp32 out, split by columns
+                L.idx_wkp = Lin(torch.cat([get(ix + "wk.weight"), get(ix + "weights_proj.weight")]), dev, fp8=False)
         f = p + "ffn."
         L.moe = cfg.is_moe_layer(i)
         if not L.moe:
@@ -447,9 +451,14 @@ class DeepseekModel:
                     R.rms_norm(kv, L.kv_norm, cfg.rms_eps)
                 latent_l = kv_c.to(self.act_dtype).contiguous()
                 C.rope_(latent_l.view(-1, 1, r), r - dr, dr, self.cos_sin, pos_l)
+            elif self.on_gpu:
+                # the projection output becomes the latent row in place: RMSNorm of the first r columns, RoPE of the
+                # last dr (no copies, no concatenation)
+                latent_l = kv
+                C.rms_norm_(latent_l[:, :r], L.kv_norm, cfg.rms_eps)
+                C.rope_(latent_l.view(-1, 1, r + dr), r, dr, self.cos_sin, pos_l)
             else:
-                kv_c = C.rms_norm(kv[:, :r].contiguous(), L.kv_norm, cfg.rms_eps) if self.on_gpu else \
-                    R.rms_norm(kv[:, :r], L.kv_norm, cfg.rms_eps)
+                kv_c = R.rms_norm(kv[:, :r], L.kv_norm, cfg.rms_eps)
                 k_pe = kv[:, r:].contiguous().view(-1, 1, dr)
                 C.rope_(k_pe, 0, dr, self.cos_sin, pos_l)
                 latent_l = torch.cat([kv_c.to(self.act_dtype), k_pe.view(-1, dr).to(self.act_dtype)], dim=-1)
@@ -535,10 +544,15 @@ class DeepseekModel:
         if not self.on_gpu:
             q = q.clone()
         C.rope_(q, 0, dr, self.cos_sin, pos)
-        k = F.layer_norm(L.idx_wk(h).float(), (Di,), L.idx_kn_w, L.idx_kn_b, 1e-6).to(self.act_dtype)
+        if self.on_gpu:
+            kw = L.idx_wkp(h, out_dtype=torch.float32)                               # [T, Di + Hi]
+            k = F.layer_norm(kw[:, :Di], (Di,), L.idx_kn_w, L.idx_kn_b, 1e-6).to(self.act_dtype)
+            w = kw[:, Di:] * ((Hi ** -0.5) * (Di ** -0.5))
+        else:
+            k = F.layer_norm(L.idx_wk(h).float(), (Di,), L.idx_kn_w, L.idx_kn_b, 1e-6).to(self.act_dtype)
+            w = (L.idx_wp(h, out_dtype=torch.float32) * (Hi ** -0.5) * (Di ** -0.5)).float()
         k = k.view(T, 1, Di)
         C.rope_(k, 0, dr, self.cos_sin, pos)
-        w = (L.idx_wp(h, out_dtype=torch.float32) * (Hi ** -0.5) * (Di ** -0.5)).float()
         if cfg.index_fp4:               # fp4 values are exact in bf16: the bf16 logits kernels compute fp4 products
             q = R.fake_quant_mxfp4(q)
             k = R.fake_quant_mxfp4(k)

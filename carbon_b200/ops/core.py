@@ -12,6 +12,17 @@ from .quant import empty_sf, pack_sf
 SCORE_FUNCS = {"sigmoid": 0, "sqrtsoftplus": 1, "softmax": 2}
 
 
+def rms_norm_(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """In-place RMSNorm of the rows of x (a bf16 [M, D] view with unit column stride, e.g. a column slice of a
+    wider projection output).  The kernel reads each element before it writes it, with one thread per element in both
+    passes, so the output may alias the input."""
+    if not x.is_cuda:
+        x.copy_(R.rms_norm(x, w, eps).to(x.dtype))
+        return x
+    ext().rms_norm(x, w, x, None, None, float(eps))
+    return x
+
+
 def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, want_bf16: bool = True, want_fp8: bool = False):
     """Returns y (bf16) and/or (q fp8, sf)."""
     if not x.is_cuda:

@@ -118,12 +118,13 @@ def _fused_one_rank():
     os.environ.setdefault("MASTER_PORT", "29517")
     if not dist.is_initialized():
         dist.init_process_group("gloo", rank=0, world_size=1)
-    return FusedCtx(0, 1, heap_bytes=12 << 30, max_tokens=16384, max_seq=4096)
+    return FusedCtx(0, 1, heap_bytes=4 << 30, max_tokens=8192, max_seq=4096)
 
 
 def ep_moe():
-    """EP MoE layer through the fused path on one rank, 16384 tokens x top-8 of 64 experts (hidden 7168): count,
-    dispatch (quantise + row stores), grouped GEMMs with the push-combine epilogue, local combine."""
+    """EP MoE layer through the fused path on one rank, 8192 tokens x top-8 of 64 experts (hidden 7168): count,
+    dispatch (quantise + row stores), grouped GEMMs with the push-combine epilogue, local combine (two pipelined
+    chunks of 4096 tokens)."""
     from .config import ModelConfig
     from .models.deepseek import DeepseekModel
     from .models.weights import WeightSource
@@ -132,7 +133,7 @@ def ep_moe():
     f = _fused_one_rank()
     cfg = ModelConfig(n_layers=1, n_dense_layers=0, vocab_size=1024, n_routed_experts=64, index_n_heads=0)
     m = DeepseekModel(cfg, WeightSource(cfg, seed=0), "cuda", pctx=f)
-    T = 16384
+    T = 8192
     h = torch.randn(T, cfg.hidden_size, device="cuda").to(torch.bfloat16)
     w, ids = C.router_topk(torch.randn(T, 64, device="cuda"), None, 8, "sigmoid", 2.5, True)
     f.set_bounds([0, T])
@@ -141,9 +142,9 @@ def ep_moe():
 
 
 def oproj_a2a():
-    """Head -> token all-to-all of 16384 tokens x 128 heads x 128 dims (bf16) on one rank (p2p_a2a_heads)."""
+    """Head -> token all-to-all of 8192 tokens x 128 heads x 128 dims (bf16) on one rank (p2p_a2a_heads)."""
     f = _fused_one_rank()
-    T = 16384
+    T = 8192
     f.set_bounds([0, T])
     o = torch.randn(T, 128, 128, device="cuda").to(torch.bfloat16)
     for _ in range(2):
