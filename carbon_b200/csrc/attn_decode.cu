@@ -31,7 +31,10 @@ constexpr int NAC_MAX = 5;             // atoms one CTA of the pair owns (value 
 constexpr int Q_ATOM = HM * 128;       // 16 KB: 128 rows x 64 dims
 constexpr int KV_ATOM = KT * 128;      // 4 KB: 32 rows x 64 dims
 constexpr int KV_STAGE = NAC_MAX * KV_ATOM;
-constexpr int X_BYTES = HM * KT * 4;   // one partial-score exchange buffer: 128 rows x 32 fp32
+// one partial-score exchange buffer: 128 rows x 32 fp32, rows padded to 36 floats so that the eight threads of a
+// quarter warp reading 16 bytes of eight consecutive rows hit eight different 4-bank groups
+constexpr int X_LD = KT + 4;
+constexpr int X_BYTES = HM * X_LD * 4;
 // TMEM: O [128 x 256] fp32 at columns [0, 256); two S buffers of 64 columns at 256 and 320 (P overwrites the first
 // KT/2 columns of its S buffer as packed bf16 and is read there by the P·V MMA)
 constexpr int TM_O = 0, TM_S = 256, TM_S_STRIDE = 64;
@@ -92,7 +95,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sKV = sQ + NAC_MAX * Q_ATOM;
-  float* xbuf = reinterpret_cast<float*>(sKV + STAGES * KV_STAGE);   // [2][128][KT]: the PEER's partial S
+  float* xbuf = reinterpret_cast<float*>(sKV + STAGES * KV_STAGE);   // [2][128][X_LD]: the PEER's partial S
   uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(xbuf) + 2 * X_BYTES);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;              // [STAGES]
@@ -225,18 +228,18 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
       const uint32_t vmask = __ballot_sync(0xffffffffu, my_slot >= 0);
       tmem_ld_wait();
       // arm this CTA's receive barrier for the peer's partial of tile j (its stores count down the bytes)
-      if (row == 0) mbar_arrive_expect_tx(&x_full[b], X_BYTES);
+      if (row == 0) mbar_arrive_expect_tx(&x_full[b], HM * KT * 4);    // 128 rows x 32 fp32 (no padding)
       // my partial -> the peer's exchange buffer b (once the peer has consumed what I wrote there two tiles ago):
       // asynchronous stores whose bytes complete the peer's x_full[b], no fence on this side
       if (!mbar_wait(&x_empty[b], ((j >> 1) & 1) ^ 1)) { fail(kErrTimeoutPeer); ok = false; break; }
-      const uint32_t xrow = mapa_shared(smem_u32(xbuf + (b * HM + row) * KT), peer);
+      const uint32_t xrow = mapa_shared(smem_u32(xbuf + (b * HM + row) * X_LD), peer);
       const uint32_t xbar = mapa_shared(smem_u32(&x_full[b]), peer);
 #pragma unroll
       for (int c = 0; c < KT / 4; ++c)
         st_async_v4(xrow + 16 * c, r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3], xbar);
       // the peer's partial of this tile
       if (!mbar_wait(&x_full[b], (j >> 1) & 1)) { fail(kErrTimeoutPeer); ok = false; break; }
-      const float4* xr = reinterpret_cast<const float4*>(xbuf + (b * HM + row) * KT);
+      const float4* xr = reinterpret_cast<const float4*>(xbuf + (b * HM + row) * X_LD);
       float sv[KT];
 #pragma unroll
       for (int c = 0; c < KT / 4; ++c) {

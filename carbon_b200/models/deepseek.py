@@ -967,8 +967,17 @@ def head_bmm(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     if not x.is_cuda:
         return torch.einsum("thk,hnk->thn", x.float(), w.float())
     Tp = ((T + 127) // 128) * 128
-    xt = torch.zeros(H, Tp, K, dtype=torch.bfloat16, device=x.device)
+    # head-major rows, each head's block padded to 128 rows; the padding rows are never read back (every output
+    # row depends only on its own input row), so they stay uninitialised
+    xt = torch.empty(H, Tp, K, dtype=torch.bfloat16, device=x.device)
     xt[:, :T] = x.transpose(0, 1)
-    mbe = torch.arange(H, dtype=torch.int32, device=x.device).repeat_interleave(Tp // 128)
+    key = (H, Tp // 128, x.device)
+    mbe = _HEAD_BLOCKS.get(key)
+    if mbe is None:
+        mbe = torch.arange(H, dtype=torch.int32, device=x.device).repeat_interleave(Tp // 128)
+        _HEAD_BLOCKS[key] = mbe
     out = bf16_gemm(xt.view(H * Tp, K), w.reshape(H * N, K), m_block_expert=mbe, n_per_group=N)
     return out.view(H, Tp, N)[:, :T].transpose(0, 1)
+
+
+_HEAD_BLOCKS: Dict[tuple, torch.Tensor] = {}      # expert (= head) of each 128-row block, per (heads, blocks, device)
