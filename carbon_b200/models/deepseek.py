@@ -723,9 +723,6 @@ class DeepseekModel:
         T, Hl = q.shape[0], self.H_local
         dn, r = cfg.qk_nope_head_dim, cfg.kv_lora_rank
         lo, hi = pc.local
-        with region("attn.absorb_q"):
-            q_abs = head_bmm(q[..., :dn], L.w_uk)                                    # [T, Hl, r]
-            qf = torch.cat([q_abs.to(self.act_dtype), q[..., dn:].to(self.act_dtype)], dim=-1).contiguous()
         # Tensor-parallel heads, but the core runs token-parallel: every rank would otherwise stream the selected
         # latent rows of ALL tokens for its few heads.  Two small all-to-alls (q in, o_lat out) let each rank read
         # only its own tokens' rows, for every head.
@@ -736,16 +733,33 @@ class DeepseekModel:
             idx = sel if local or pc.world == 1 else pc.gather_rows(sel)
         else:
             idx = fb.key_slots[lo:hi] if local else fb.key_slots
+        pending = None
         if sel is None and src is not None and int(fb.key_slots.shape[1]) > cfg.index_topk:
             if src == i:
-                with region("attn.indexer_topk"):
-                    qi, _, wi = idx_l
-                    sel = A.indexer_topk(qi, wi, cache.index_k[i], fb.key_slots[lo:hi].contiguous(),
-                                         fb.n_keys[lo:hi].contiguous(), cfg.index_topk)
-                    idx = sel if local else pc.gather_rows(sel)
-                self._dsa[i] = idx
+                qi, _, wi = idx_l
+                ks, nk = fb.key_slots[lo:hi].contiguous(), fb.n_keys[lo:hi].contiguous()
+                if self.on_gpu and local:
+                    # the DSA selection runs on a side stream, overlapping the query absorption below (the
+                    # reference's decode index streams)
+                    side = self._index_stream()
+                    side.wait_stream(torch.cuda.current_stream())
+                    for t_ in (qi, wi, ks, nk):
+                        t_.record_stream(side)
+                    with torch.cuda.stream(side), region("attn.indexer_topk"):
+                        pending = Pending(A.indexer_topk(qi, wi, cache.index_k[i], ks, nk, cfg.index_topk), side)
+                else:
+                    with region("attn.indexer_topk"):
+                        sel = A.indexer_topk(qi, wi, cache.index_k[i], ks, nk, cfg.index_topk)
+                        idx = sel if local else pc.gather_rows(sel)
+                    self._dsa[i] = idx
             else:
                 idx = self._dsa[src]                # selection shared with the index-source layer
+        with region("attn.absorb_q"):
+            q_abs = head_bmm(q[..., :dn], L.w_uk)                                    # [T, Hl, r]
+            qf = torch.cat([q_abs.to(self.act_dtype), q[..., dn:].to(self.act_dtype)], dim=-1).contiguous()
+        if pending is not None:
+            idx = pending.get()
+            self._dsa[i] = idx
         if swap:
             with region("attn.core_decode"):
                 q_tok = pc.heads_to_tokens(qf)                                      # [n_r, H, r + dr]
@@ -762,6 +776,11 @@ class DeepseekModel:
                 o_lat = A.sparse_mla(qf, cache.latent[i], idx.contiguous(), cfg.softmax_scale, r, sink=L.sink)
         with region("attn.absorb_o"):
             return head_bmm(o_lat, L.w_uv), False                                    # [T, Hl, dv]
+
+    def _index_stream(self):
+        if getattr(self, "_idx_side", None) is None:
+            self._idx_side = torch.cuda.Stream()
+        return self._idx_side
 
     # ------------------------------------------------------------------------------------------------------------------
     # FFN
