@@ -90,6 +90,7 @@ template <int NA>
 __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constant__ CUtensorMap tm_q,
                                                             const __grid_constant__ CUtensorMap tm_kv,
                                                             const Params p) {
+  cb::pdl_entry();
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 1000
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -351,6 +352,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
 // out[t, h, :] = Σ_s 2^(m_s - M) O_s / Σ_s 2^(m_s - M) l_s
 __global__ void mla_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int n_splits,
                                    int H, __nv_bfloat16* __restrict__ out, const float* __restrict__ sink) {
+  cb::pdl_entry();
   const int t = blockIdx.x, h = blockIdx.y;
   float M = -INFINITY;
   for (int s = 0; s < n_splits; ++s) M = fmaxf(M, part_ml[((size_t(t) * n_splits + s) * H + h) * 2]);
@@ -432,16 +434,18 @@ cudaError_t sparse_mla(const void* q, int T, int H, const void* kv, int S, const
   p.out = reinterpret_cast<__nv_bfloat16*>(out);
   p.status = status;
   p.sink = sink;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1; attr[0].val.clusterDim.y = 2; attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;     // see cb::pdl_entry
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(T, 2, n_splits);
   cfg.blockDim = dim3(256);
   cfg.dynamicSmemBytes = SMEM;
   cfg.stream = s;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   {
     cudaError_t e = D == 576 ? cudaLaunchKernelEx(&cfg, sparse_mla_kernel<9>, tq, tkv, p)
                              : cudaLaunchKernelEx(&cfg, sparse_mla_kernel<8>, tq, tkv, p);
@@ -449,7 +453,7 @@ cudaError_t sparse_mla(const void* q, int T, int H, const void* kv, int S, const
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || n_splits == 1) return e;
-  mla_combine_kernel<<<dim3(T, H), 128, 0, s>>>(part_o, part_ml, n_splits, H, reinterpret_cast<__nv_bfloat16*>(out),
+  cb::launch_k(mla_combine_kernel, dim3(T, H), 128, 0, s, part_o, part_ml, n_splits, H, reinterpret_cast<__nv_bfloat16*>(out),
                                                 sink);
   return cudaGetLastError();
 }

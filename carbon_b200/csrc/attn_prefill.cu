@@ -90,6 +90,7 @@ __global__ void __launch_bounds__(384, 1) attn_prefill_kernel(const __grid_const
                                                               const __grid_constant__ CUtensorMap tm_kv,
                                                               const __grid_constant__ CUtensorMap tm_kpe,
                                                               const Params p) {
+  cb::pdl_entry();
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 1000
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -373,6 +374,7 @@ __global__ void __launch_bounds__(384, 1) attn_prefill2_kernel(const __grid_cons
                                                                const __grid_constant__ CUtensorMap tm_kv,
                                                                const __grid_constant__ CUtensorMap tm_kpe,
                                                                const fa::Params p) {
+  cb::pdl_entry();
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 1000
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -660,6 +662,7 @@ __global__ void __launch_bounds__(384, 1) attn_prefill3_kernel(const __grid_cons
                                                                const __grid_constant__ CUtensorMap tm_kv,
                                                                const __grid_constant__ CUtensorMap tm_kpe,
                                                                const fa::Params p) {
+  cb::pdl_entry();
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 1000
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -986,7 +989,7 @@ cudaError_t attn_prefill(const void* q, const void* kvb, const void* kpe, int T,
   p.trace_cap = 0;
   p.sink = sink;
   dim3 grid(n_tiles, H);
-  attn_prefill_kernel<<<grid, 384, SMEM, s>>>(tq, tkv, tkpe, p);
+  cb::launch_k(attn_prefill_kernel, grid, 384, SMEM, s, tq, tkv, tkpe, p);
   return cudaGetLastError();
 }
 
@@ -1018,7 +1021,7 @@ cudaError_t attn_prefill2(const void* q, const void* kvb, const void* kpe, int T
   p.trace_cap = trace_cap;
   p.sink = sink;
   dim3 grid(n_tiles, H);
-  fa2::attn_prefill2_kernel<<<grid, 384, fa2::SMEM, s>>>(tq, tkv, tkpe, p);
+  cb::launch_k(fa2::attn_prefill2_kernel, grid, 384, fa2::SMEM, s, tq, tkv, tkpe, p);
   return cudaGetLastError();
 }
 
@@ -1050,7 +1053,7 @@ cudaError_t attn_prefill3(const void* q, const void* kvb, const void* kpe, int T
   p.trace_cap = trace_cap;
   p.sink = sink;
   dim3 grid(n_tiles, H);
-  fa3::attn_prefill3_kernel<<<grid, 384, fa3::SMEM, s>>>(tq, tkv, tkpe, p);
+  cb::launch_k(fa3::attn_prefill3_kernel, grid, 384, fa3::SMEM, s, tq, tkv, tkpe, p);
   return cudaGetLastError();
 }
 

@@ -6,6 +6,7 @@
 #include <cuda_fp8.h>
 #include <stdint.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <map>
 #include <mutex>
 #include <utility>
@@ -143,6 +144,47 @@ template <typename F>
 inline cudaError_t smem_optin(F* fn, int bytes) {
   return smem_optin(reinterpret_cast<const void*>(fn), bytes);
 }
+
+// Programmatic dependent launch.  Every kernel of this library starts with pdl_entry(): it waits until the kernel
+// launched before it in the stream has completed and its memory is visible (a no-op when this launch carries no
+// programmatic dependency), then lets the next kernel of the stream be launched early, so that its launch and
+// prologue overlap this kernel's work.  Waiting first keeps the dependency transitive: a kernel can never finish
+// before its predecessor has.
+CB_DEVICE void pdl_entry() {
+#if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 900
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+#endif
+}
+
+// Whether launches carry the programmatic-serialization attribute (CARBON_PDL=0 turns it off).
+inline bool pdl_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("CARBON_PDL");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+#ifdef __CUDACC__
+// Kernel launch with programmatic stream serialization (see pdl_entry); returns the launch's error code.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s,
+                            Args&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+#endif
 
 CB_HOST_DEVICE int ceil_div(int a, int b) { return (a + b - 1) / b; }
 CB_HOST_DEVICE int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }

@@ -21,6 +21,7 @@ namespace cb {
 __global__ void engram_gather_kernel(const int* __restrict__ ids, int T, int C, int dim,
                                      const uint64_t* __restrict__ data_ptrs, const uint64_t* __restrict__ sf_ptrs,
                                      const int* __restrict__ bounds, int world, __nv_bfloat16* __restrict__ out) {
+  cb::pdl_entry();
   const int warps = blockDim.x >> 5;
   const int item = blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -62,7 +63,7 @@ cudaError_t engram_gather(const int* ids, int T, int C, int dim, const uint64_t*
   if (dim % 32) return cudaErrorInvalidValue;
   const int items = T * C;
   const int warps = 8;
-  engram_gather_kernel<<<(items + warps - 1) / warps, 32 * warps, 0, s>>>(
+  cb::launch_k(engram_gather_kernel, (items + warps - 1) / warps, 32 * warps, 0, s, 
       ids, T, C, dim, data_ptrs, sf_ptrs, bounds, world, reinterpret_cast<__nv_bfloat16*>(out));
   return cudaGetLastError();
 }
@@ -89,6 +90,7 @@ __global__ void engram_gate_kernel(__nv_bfloat16* __restrict__ X, const __nv_bfl
                                    const float* __restrict__ qw, const float* __restrict__ kw, int hc, int D,
                                    float eps, float clamp, float* __restrict__ sumsq, const int* __restrict__ tok,
                                    int img_id) {
+  cb::pdl_entry();
   __shared__ float red[33];
   const int t = blockIdx.x;
   const bool skip = tok != nullptr && tok[t] == img_id;          // image tokens take no n-gram update
@@ -125,7 +127,7 @@ __global__ void engram_gate_kernel(__nv_bfloat16* __restrict__ X, const __nv_bfl
 cudaError_t engram_gate(void* X, const void* kv, const float* qw, const float* kw, int T, int hc, int D, float eps,
                         float clamp, float* sumsq, cudaStream_t s, const int* tok, int img_id) {
   if (T == 0) return cudaSuccess;
-  engram_gate_kernel<<<T, 256, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(X),
+  cb::launch_k(engram_gate_kernel, T, 256, 0, s, reinterpret_cast<__nv_bfloat16*>(X),
                                        reinterpret_cast<const __nv_bfloat16*>(kv), qw, kw, hc, D, eps, clamp, sumsq,
                                        tok, img_id);
   return cudaGetLastError();

@@ -73,9 +73,11 @@ static cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, con
   static_assert(smem <= 227 * 1024, "pair GEMM shared memory above the per-CTA limit");
   auto kern = gemm_pair_kernel<KIND, EPI, PAIR, ST>;
   static int resident = 0;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = PAIR; attr[0].val.clusterDim.y = 1; attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;     // see cb::pdl_entry
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(C::kThreads);
   cfg.dynamicSmemBytes = smem;
@@ -98,11 +100,13 @@ static cudaError_t launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, con
   const int units = max_units < resident ? max_units : resident;
   if (units <= 0) return cudaSuccess;
   cfg.gridDim = dim3(units * PAIR);
+  cfg.numAttrs = cb::pdl_enabled() ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, kern, ta, tb, tsa, tsb, p);
 }
 
 __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits, int M, int N, int ldo,
                                      float* __restrict__ out) {
+  cb::pdl_entry();
   const int64_t total = int64_t(M) * N;
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
     const int r = int(i / N), c = int(i % N);
@@ -115,7 +119,7 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ part, int splits,
 static cudaError_t splitk_reduce(const float* part, int splits, int M, int N, int ldo, float* out, cudaStream_t s) {
   const int64_t total = int64_t(M) * N;
   const int blocks = int(total / 256 + 1 < 1024 ? total / 256 + 1 : 1024);
-  splitk_reduce_kernel<<<blocks, 256, 0, s>>>(part, splits, M, N, ldo, out);
+  cb::launch_k(splitk_reduce_kernel, blocks, 256, 0, s, part, splits, M, N, ldo, out);
   return cudaGetLastError();
 }
 
@@ -123,6 +127,7 @@ static cudaError_t splitk_reduce(const float* part, int splits, int M, int N, in
 template <int MODE>
 __global__ void splitk_reduce_out_kernel(const float* __restrict__ part, int splits, int M, int N, void* out,
                                          int ldo) {
+  cb::pdl_entry();
   const int64_t total4 = int64_t(M) * (N / 4);
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total4; i += int64_t(gridDim.x) * blockDim.x) {
     const int r = int(i / (N / 4)), c = int(i % (N / 4)) * 4;
@@ -146,6 +151,7 @@ __global__ void splitk_reduce_swiglu_kernel(const float* __restrict__ part, int 
                                             uint8_t* __restrict__ out, int ldo, uint32_t* __restrict__ out_sf,
                                             int sf_row_blocks, const int* __restrict__ row_valid,
                                             const int* __restrict__ n_blocks) {
+  cb::pdl_entry();
   const int I = N / 2, chunks = I / 128;
   const int wg = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -214,7 +220,7 @@ static cudaError_t launch(const CUtensorMap& ta, const CUtensorMap& tb, const Ge
   }
   const int grid = max_tiles < num_sms ? max_tiles : num_sms;
   if (grid <= 0) return cudaSuccess;
-  kern<<<grid, 256, smem, s>>>(ta, tb, p);
+  cb::launch_k(kern, grid, 256, smem, s, ta, tb, p);
   return cudaGetLastError();
 }
 
@@ -271,7 +277,7 @@ cudaError_t gemm_fp8(const void* A, const void* B, const uint32_t* sfa, const ui
       cudaError_t e = launch<KIND_MXF8, EPI_F32, 128, 6, 2>(ta, tb, p, max_tiles, num_sms, s);
       if (e != cudaSuccess) return e;
       const int warps = M * (N / 256);
-      splitk_reduce_swiglu_kernel<<<ceil_div(warps, 8), 256, 0, s>>>(work, 1, M, N, swiglu_limit,
+      cb::launch_k(splitk_reduce_swiglu_kernel, ceil_div(warps, 8), 256, 0, s, work, 1, M, N, swiglu_limit,
                                                                      reinterpret_cast<uint8_t*>(out), ldo, out_sf,
                                                                      ceil_div(M, 128), row_valid, num_m_blocks_dev);
       return cudaGetLastError();
@@ -301,14 +307,14 @@ cudaError_t gemm_fp8(const void* A, const void* B, const uint32_t* sfa, const ui
     const int used = ceil_div(nk_total, nk_per);
     if (epi == GEMM_OUT_SWIGLU_FP8) {
       const int warps = M * (N / 256);
-      splitk_reduce_swiglu_kernel<<<ceil_div(warps, 8), 256, 0, s>>>(work, used, M, N, swiglu_limit,
+      cb::launch_k(splitk_reduce_swiglu_kernel, ceil_div(warps, 8), 256, 0, s, work, used, M, N, swiglu_limit,
                                                                      reinterpret_cast<uint8_t*>(out), ldo, out_sf,
                                                                      ceil_div(M, 128), nullptr, nullptr);
     } else {
       const int64_t total4 = int64_t(M) * (N / 4);
       const int blocks = int(total4 / 256 + 1 < 1024 ? total4 / 256 + 1 : 1024);
-      if (epi == GEMM_OUT_F32) splitk_reduce_out_kernel<0><<<blocks, 256, 0, s>>>(work, used, M, N, out, ldo);
-      else splitk_reduce_out_kernel<1><<<blocks, 256, 0, s>>>(work, used, M, N, out, ldo);
+      if (epi == GEMM_OUT_F32) cb::launch_k(splitk_reduce_out_kernel<0>, blocks, 256, 0, s, work, used, M, N, out, ldo);
+      else cb::launch_k(splitk_reduce_out_kernel<1>, blocks, 256, 0, s, work, used, M, N, out, ldo);
     }
     return cudaGetLastError();
   }

@@ -71,6 +71,7 @@ template <int KIND, int EPI, int BLOCK_N, int STAGES, int ACC_STAGES>
 __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                          const __grid_constant__ CUtensorMap tmap_b,
                                                          const GemmParams p) {
+  cb::pdl_entry();
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 1000
   using S = GemmSmem<BLOCK_N>;
   constexpr int BLOCK_M = 128;

@@ -72,6 +72,7 @@ __global__ void __launch_bounds__(PairCfg<KIND, PAIR, EPI>::kThreads, 1)
     gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                      const __grid_constant__ CUtensorMap tmap_sfa, const __grid_constant__ CUtensorMap tmap_sfb,
                      const GemmParams p) {
+  cb::pdl_entry();
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 1000
   using C = PairCfg<KIND, PAIR, EPI>;
   constexpr int BN = C::BN, BM = C::BM, BK = C::BK;

@@ -52,6 +52,7 @@ CB_DEVICE void tma_gather4(void* dst, const void* tmap, uint64_t* bar, int col, 
 __global__ void __launch_bounds__(192) indexer_decode_kernel(const __grid_constant__ CUtensorMap tm_q,
                                                               const __grid_constant__ CUtensorMap tm_k,
                                                               const Params p) {
+  cb::pdl_entry();
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 1000
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -228,7 +229,7 @@ cudaError_t indexer_decode_logits(const void* q, const float* w, const void* kc,
   p.key_slots = key_slots; p.n_keys = n_keys; p.w = w; p.out = out;
   p.Lmax = Lmax; p.H = H; p.tiles = (Lmax + KT - 1) / KT; p.status = status;
   dim3 grid(T, (p.tiles + TILES_PER_CTA - 1) / TILES_PER_CTA);
-  indexer_decode_kernel<<<grid, 192, smem, s>>>(tq, tk, p);
+  cb::launch_k(indexer_decode_kernel, grid, 192, smem, s, tq, tk, p);
   return cudaGetLastError();
 }
 

@@ -24,6 +24,7 @@ namespace cb {
 template <typename V>
 __global__ void p2p_gather_kernel(const uint8_t* __restrict__ src, int n, int row_bytes,
                                   const uint64_t* __restrict__ dst_ptrs, int world, int row0) {
+  cb::pdl_entry();
   const int chunks = row_bytes / int(sizeof(V));
   const int64_t total = int64_t(n) * chunks;
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
@@ -45,10 +46,10 @@ cudaError_t p2p_gather_rows(const void* src, int n, int row_bytes, const uint64_
   const int64_t total = int64_t(n) * (row_bytes / (wide ? 16 : 4));
   const int blocks = int(total / 256 + 1 < 4 * 148 ? total / 256 + 1 : 4 * 148);
   if (wide)
-    p2p_gather_kernel<uint4><<<blocks, 256, 0, s>>>(reinterpret_cast<const uint8_t*>(src), n, row_bytes, dst_ptrs,
+    cb::launch_k(p2p_gather_kernel<uint4>, blocks, 256, 0, s, reinterpret_cast<const uint8_t*>(src), n, row_bytes, dst_ptrs,
                                                     world, row0);
   else
-    p2p_gather_kernel<uint32_t><<<blocks, 256, 0, s>>>(reinterpret_cast<const uint8_t*>(src), n, row_bytes,
+    cb::launch_k(p2p_gather_kernel<uint32_t>, blocks, 256, 0, s, reinterpret_cast<const uint8_t*>(src), n, row_bytes,
                                                        dst_ptrs, world, row0);
   return cudaGetLastError();
 }
@@ -64,6 +65,7 @@ cudaError_t p2p_gather_rows(const void* src, int n, int row_bytes, const uint64_
 // ---------------------------------------------------------------------------------------------------------------
 __global__ void p2p_a2a_heads_kernel(const uint8_t* __restrict__ src, const int* __restrict__ bounds, int world,
                                      int my_rank, const uint64_t* __restrict__ dst_ptrs, int C, int mode) {
+  cb::pdl_entry();
   const int i = blockIdx.x, d = blockIdx.y;
   const uint8_t* s;
   uint8_t* t;
@@ -87,7 +89,7 @@ cudaError_t p2p_a2a_heads(const void* src, const int* bounds_dev, int world, int
                           int C, int mode, int max_rows, cudaStream_t s) {
   if (max_rows <= 0) return cudaSuccess;
   if (C % 16 || (mode != 0 && mode != 1)) return cudaErrorInvalidValue;
-  p2p_a2a_heads_kernel<<<dim3(max_rows, world), 256, 0, s>>>(reinterpret_cast<const uint8_t*>(src), bounds_dev,
+  cb::launch_k(p2p_a2a_heads_kernel, dim3(max_rows, world), 256, 0, s, reinterpret_cast<const uint8_t*>(src), bounds_dev,
                                                              world, my_rank, dst_ptrs, C, mode);
   return cudaGetLastError();
 }
@@ -99,6 +101,7 @@ cudaError_t p2p_a2a_heads(const void* src, const int* bounds_dev, int world, int
 __global__ void p2p_scatter_kernel(const __nv_bfloat16* __restrict__ part, int D, const int* __restrict__ bounds,
                                    int world, int my_rank, const uint64_t* __restrict__ slot_ptrs, int slot_rows,
                                    int T) {
+  cb::pdl_entry();
   const int chunks = D / 8;
   const int64_t total = int64_t(T) * chunks;
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
@@ -115,6 +118,7 @@ __global__ void p2p_scatter_kernel(const __nv_bfloat16* __restrict__ part, int D
 
 __global__ void reduce_slots_kernel(const __nv_bfloat16* __restrict__ slots, int world, int slot_rows, int n, int D,
                                     __nv_bfloat16* __restrict__ out) {
+  cb::pdl_entry();
   const int chunks = D / 8;
   const int64_t total = int64_t(n) * chunks;
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total; i += int64_t(gridDim.x) * blockDim.x) {
@@ -138,7 +142,7 @@ cudaError_t p2p_scatter_partials(const void* part, int T, int D, const int* boun
   if (D % 8) return cudaErrorInvalidValue;
   const int64_t total = int64_t(T) * (D / 8);
   const int blocks = int(total / 256 + 1 < 4 * 148 ? total / 256 + 1 : 4 * 148);
-  p2p_scatter_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(part), D, bounds_dev, world,
+  cb::launch_k(p2p_scatter_kernel, blocks, 256, 0, s, reinterpret_cast<const __nv_bfloat16*>(part), D, bounds_dev, world,
                                             my_rank, slot_ptrs, slot_rows, T);
   return cudaGetLastError();
 }
@@ -147,7 +151,7 @@ cudaError_t reduce_slots(const void* slots, int world, int slot_rows, int n, int
   if (n == 0) return cudaSuccess;
   const int64_t total = int64_t(n) * (D / 8);
   const int blocks = int(total / 256 + 1 < 4 * 148 ? total / 256 + 1 : 4 * 148);
-  reduce_slots_kernel<<<blocks, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(slots), world, slot_rows, n, D,
+  cb::launch_k(reduce_slots_kernel, blocks, 256, 0, s, reinterpret_cast<const __nv_bfloat16*>(slots), world, slot_rows, n, D,
                                              reinterpret_cast<__nv_bfloat16*>(out));
   return cudaGetLastError();
 }
@@ -161,6 +165,7 @@ cudaError_t reduce_slots(const void* slots, int world, int slot_rows, int n, int
 // receive buffer by itself (no second exchange of offsets).
 __global__ void moe_count_kernel(const int* __restrict__ ids, int Tk, int E, int world, int my_rank,
                                  const uint64_t* __restrict__ cnt_ptrs, int* __restrict__ pair_rank) {
+  cb::pdl_entry();
   constexpr int kPer = 8;                  // consecutive pairs per thread per pass
   __shared__ int sw[32];
   const int e = blockIdx.x;
@@ -211,7 +216,7 @@ __global__ void moe_count_kernel(const int* __restrict__ ids, int Tk, int E, int
 cudaError_t moe_count(const int* ids, int Tk, int E, int world, int my_rank, const uint64_t* cnt_ptrs,
                       int* pair_rank, cudaStream_t s) {
   if (world > 512) return cudaErrorInvalidValue;
-  moe_count_kernel<<<E, 512, 0, s>>>(ids, Tk, E, world, my_rank, cnt_ptrs, pair_rank);
+  cb::launch_k(moe_count_kernel, E, 512, 0, s, ids, Tk, E, world, my_rank, cnt_ptrs, pair_rank);
   return cudaGetLastError();
 }
 
@@ -223,6 +228,7 @@ cudaError_t moe_count(const int* ids, int Tk, int E, int world, int my_rank, con
 __global__ void moe_layout_kernel(const int* __restrict__ cnt, int world, int E, int my_rank, int max_blocks,
                                   int align, int* __restrict__ my_off, int* __restrict__ m_block_expert,
                                   int* __restrict__ num_blocks) {
+  cb::pdl_entry();
   const int o = threadIdx.x;
   if (o >= world) return;
   const int El = E / world;
@@ -250,7 +256,7 @@ __global__ void moe_layout_kernel(const int* __restrict__ cnt, int world, int E,
 cudaError_t moe_layout(const int* cnt, int world, int E, int my_rank, int max_blocks, int align, int* my_off,
                        int* m_block_expert, int* num_blocks, cudaStream_t s) {
   if ((align != 128 && align != 256) || world > 1024 || E % world) return cudaErrorInvalidValue;
-  moe_layout_kernel<<<1, ((world + 31) / 32) * 32, 0, s>>>(cnt, world, E, my_rank, max_blocks, align, my_off,
+  cb::launch_k(moe_layout_kernel, 1, ((world + 31) / 32) * 32, 0, s, cnt, world, E, my_rank, max_blocks, align, my_off,
                                                            m_block_expert, num_blocks);
   return cudaGetLastError();
 }
@@ -266,6 +272,7 @@ __global__ void moe_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int D, 
                                     const uint64_t* __restrict__ recv_ptrs, const uint64_t* __restrict__ sf_ptrs,
                                     const int* __restrict__ my_off, const uint64_t* __restrict__ rinfo_ptrs,
                                     int cap, int* __restrict__ pos_out, int* __restrict__ status) {
+  cb::pdl_entry();
   const int t = blockIdx.x;
   const int row_blocks = cap / 128;
   __shared__ int s_dst[16], s_owner[16];
@@ -329,7 +336,7 @@ cudaError_t moe_dispatch(const void* x, int T, int D, const int* ids, int k, int
                          cudaStream_t s) {
   if (T == 0) return cudaSuccess;
   if (D % 128 || D > 64 * 512 || k > 16 || cap % 128 || (rinfo_ptrs && T * k > (1 << 24))) return cudaErrorInvalidValue;
-  moe_dispatch_kernel<<<T, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), D, ids, k, El, my_rank, pair_rank,
+  cb::launch_k(moe_dispatch_kernel, T, 256, 0, s, reinterpret_cast<const __nv_bfloat16*>(x), D, ids, k, El, my_rank, pair_rank,
                                         recv_ptrs, sf_ptrs, my_off, rinfo_ptrs, cap, pos_out, status);
   return cudaGetLastError();
 }
@@ -340,6 +347,7 @@ template <int KMAX>
 __global__ void moe_combine_slots_kernel(const __nv_bfloat16* __restrict__ slots, int D, const int* __restrict__ pos,
                                          const float* __restrict__ w, int k, const __nv_bfloat16* __restrict__ add,
                                          __nv_bfloat16* __restrict__ out) {
+  cb::pdl_entry();
   const int t = blockIdx.x;
   __shared__ float s_w[KMAX];
   if (threadIdx.x < KMAX) {
@@ -383,9 +391,9 @@ cudaError_t moe_combine_slots(const void* slots, int T, int D, const int* pos, c
   const auto* a = reinterpret_cast<const __nv_bfloat16*>(add);
   auto* o = reinterpret_cast<__nv_bfloat16*>(out);
   if (k <= 8)
-    moe_combine_slots_kernel<8><<<T, 128, 0, s>>>(sl, D, pos, w, k, a, o);
+    cb::launch_k(moe_combine_slots_kernel<8>, T, 128, 0, s, sl, D, pos, w, k, a, o);
   else
-    moe_combine_slots_kernel<16><<<T, 128, 0, s>>>(sl, D, pos, w, k, a, o);
+    cb::launch_k(moe_combine_slots_kernel<16>, T, 128, 0, s, sl, D, pos, w, k, a, o);
   return cudaGetLastError();
 }
 
@@ -396,6 +404,7 @@ template <int KMAX>
 __global__ void moe_combine_pull_kernel(const uint64_t* __restrict__ y_ptrs, int D, const int* __restrict__ ids,
                                         const int* __restrict__ pos, const float* __restrict__ w, int k, int El,
                                         const __nv_bfloat16* __restrict__ add, __nv_bfloat16* __restrict__ out) {
+  cb::pdl_entry();
   const int t = blockIdx.x;
   __shared__ const uint4* s_src[KMAX];
   __shared__ float s_w[KMAX];
@@ -442,9 +451,9 @@ cudaError_t moe_combine_pull(const uint64_t* y_ptrs, int T, int D, const int* id
   const auto* a = reinterpret_cast<const __nv_bfloat16*>(add);
   auto* o = reinterpret_cast<__nv_bfloat16*>(out);
   if (k <= 8)
-    moe_combine_pull_kernel<8><<<T, 128, 0, s>>>(y_ptrs, D, ids, pos, w, k, El, a, o);
+    cb::launch_k(moe_combine_pull_kernel<8>, T, 128, 0, s, y_ptrs, D, ids, pos, w, k, El, a, o);
   else
-    moe_combine_pull_kernel<16><<<T, 128, 0, s>>>(y_ptrs, D, ids, pos, w, k, El, a, o);
+    cb::launch_k(moe_combine_pull_kernel<16>, T, 128, 0, s, y_ptrs, D, ids, pos, w, k, El, a, o);
   return cudaGetLastError();
 }
 
@@ -454,6 +463,7 @@ cudaError_t moe_combine_pull(const uint64_t* y_ptrs, int T, int D, const int* id
 __global__ void embed_peer_kernel(const uint64_t* __restrict__ table_ptrs, int per, int world,
                                   const int* __restrict__ ids, int D, int hc, __nv_bfloat16* __restrict__ X,
                                   float* __restrict__ sumsq) {
+  cb::pdl_entry();
   __shared__ float red[32];
   const int t = blockIdx.x;
   int id = ids[t];
@@ -476,7 +486,7 @@ __global__ void embed_peer_kernel(const uint64_t* __restrict__ table_ptrs, int p
 cudaError_t embed_peer(const uint64_t* table_ptrs, int per, int world, const int* ids, int T, int D, int hc,
                        void* X, float* sumsq, cudaStream_t s) {
   if (T == 0) return cudaSuccess;
-  embed_peer_kernel<<<T, 128, 0, s>>>(table_ptrs, per, world, ids, D, hc, reinterpret_cast<__nv_bfloat16*>(X),
+  cb::launch_k(embed_peer_kernel, T, 128, 0, s, table_ptrs, per, world, ids, D, hc, reinterpret_cast<__nv_bfloat16*>(X),
                                       sumsq);
   return cudaGetLastError();
 }

@@ -25,6 +25,7 @@ __global__ void act_quant_kernel(const __nv_bfloat16* __restrict__ x, int ldx, u
                                  uint32_t* __restrict__ sf, int M, int K, int row_blocks,
                                  const int* __restrict__ src_rows, int M_pad, const int* __restrict__ n_blocks,
                                  int x_rows) {
+  cb::pdl_entry();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.y * 8 + warp;
   const int kg = blockIdx.x;
@@ -85,7 +86,7 @@ cudaError_t act_quant(const void* x, int ldx, void* q, int ldq, uint32_t* sf, in
   if (x_rows < 0) x_rows = 0x7fffffff;
   const int row_blocks = ceil_div(M, 128), M_pad = row_blocks * 128;
   dim3 grid(ceil_div(K, 512), ceil_div(M_pad, 8));
-  act_quant_kernel<<<grid, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), ldx,
+  cb::launch_k(act_quant_kernel, grid, 256, 0, s, reinterpret_cast<const __nv_bfloat16*>(x), ldx,
                                         reinterpret_cast<uint8_t*>(q), ldq, sf, M, K, row_blocks, src_rows, M_pad,
                                         n_blocks, x_rows);
   return cudaGetLastError();
@@ -98,6 +99,7 @@ __global__ void gather_fp8_rows_kernel(const uint8_t* __restrict__ src, const ui
                                        int src_rows_n, int K, const int* __restrict__ src_rows, int M,
                                        const int* __restrict__ n_blocks, uint8_t* __restrict__ dst,
                                        uint32_t* __restrict__ dst_sf) {
+  cb::pdl_entry();
   const int row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
@@ -119,7 +121,7 @@ __global__ void gather_fp8_rows_kernel(const uint8_t* __restrict__ src, const ui
 cudaError_t gather_fp8_rows(const void* src, const uint32_t* src_sf, int src_rows_n, int K, const int* src_rows,
                             int M, const int* n_blocks, void* dst, uint32_t* dst_sf, cudaStream_t s) {
   if (K % 16) return cudaErrorInvalidValue;
-  gather_fp8_rows_kernel<<<ceil_div(M, 8), 256, 0, s>>>(reinterpret_cast<const uint8_t*>(src), src_sf, src_rows_n,
+  cb::launch_k(gather_fp8_rows_kernel, ceil_div(M, 8), 256, 0, s, reinterpret_cast<const uint8_t*>(src), src_sf, src_rows_n,
                                                         K, src_rows, M, n_blocks, reinterpret_cast<uint8_t*>(dst),
                                                         dst_sf);
   return cudaGetLastError();
@@ -133,6 +135,7 @@ template <int MAXV>
 __global__ void rms_norm_kernel(const __nv_bfloat16* __restrict__ x, int ldx, const float* __restrict__ w,
                                 __nv_bfloat16* __restrict__ y, int ldy, uint8_t* __restrict__ q, uint32_t* sf,
                                 int row_blocks, int D, float eps) {
+  cb::pdl_entry();
   __shared__ float red[32];
   const int row = blockIdx.x;
   const __nv_bfloat16* xr = x + size_t(row) * ldx;
@@ -200,15 +203,16 @@ cudaError_t rms_norm(const void* x, int ldx, const float* w, void* y, int ldy, v
   auto yy = reinterpret_cast<__nv_bfloat16*>(y);
   auto qq = reinterpret_cast<uint8_t*>(q);
   if (q && D % 128) return cudaErrorInvalidValue;
-  if (per <= 1) rms_norm_kernel<1><<<M, 256, 0, s>>>(xx, ldx, w, yy, ldy, qq, sf, rb, D, eps);
-  else if (per <= 2) rms_norm_kernel<2><<<M, 256, 0, s>>>(xx, ldx, w, yy, ldy, qq, sf, rb, D, eps);
-  else if (per <= 4) rms_norm_kernel<4><<<M, 256, 0, s>>>(xx, ldx, w, yy, ldy, qq, sf, rb, D, eps);
+  if (per <= 1) cb::launch_k(rms_norm_kernel<1>, M, 256, 0, s, xx, ldx, w, yy, ldy, qq, sf, rb, D, eps);
+  else if (per <= 2) cb::launch_k(rms_norm_kernel<2>, M, 256, 0, s, xx, ldx, w, yy, ldy, qq, sf, rb, D, eps);
+  else if (per <= 4) cb::launch_k(rms_norm_kernel<4>, M, 256, 0, s, xx, ldx, w, yy, ldy, qq, sf, rb, D, eps);
   else return cudaErrorInvalidValue;
   return cudaGetLastError();
 }
 
 // SF padding rows (>= M inside the last 128-row block) get scale bytes 127 so every SF tile is defined.
 __global__ void sf_pad_kernel(uint32_t* sf, int M, int K, int row_blocks) {
+  cb::pdl_entry();
   const int kg = blockIdx.x;
   const int r = (M & 127) + threadIdx.x;
   if ((M & 127) == 0 || r >= 128) return;
@@ -218,7 +222,7 @@ __global__ void sf_pad_kernel(uint32_t* sf, int M, int K, int row_blocks) {
 cudaError_t sf_pad(uint32_t* sf, int M, int K, cudaStream_t s) {
   const int rb = ceil_div(M, 128);
   if ((M & 127) == 0) return cudaSuccess;
-  sf_pad_kernel<<<ceil_div(K, 512), 128, 0, s>>>(sf, M, K, rb);
+  cb::launch_k(sf_pad_kernel, ceil_div(K, 512), 128, 0, s, sf, M, K, rb);
   return cudaGetLastError();
 }
 
@@ -228,6 +232,7 @@ cudaError_t sf_pad(uint32_t* sf, int M, int K, cudaStream_t s) {
 // ---------------------------------------------------------------------------------------------------------------
 __global__ void rope_kernel(__nv_bfloat16* x, int64_t stride_t, int64_t stride_h, int H, int off, int dim,
                             const float* __restrict__ cos_sin, const int* __restrict__ pos, int inverse) {
+  cb::pdl_entry();
   const int t = blockIdx.x;
   const int p = pos[t];
   const int pairs = dim / 2;
@@ -245,7 +250,7 @@ __global__ void rope_kernel(__nv_bfloat16* x, int64_t stride_t, int64_t stride_h
 cudaError_t rope_inplace(void* x, int T, int64_t stride_t, int64_t stride_h, int H, int off, int dim,
                          const float* cos_sin, const int* pos, bool inverse, cudaStream_t s) {
   if (T == 0) return cudaSuccess;
-  rope_kernel<<<T, 128, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(x), stride_t, stride_h, H, off, dim, cos_sin, pos,
+  cb::launch_k(rope_kernel, T, 128, 0, s, reinterpret_cast<__nv_bfloat16*>(x), stride_t, stride_h, H, off, dim, cos_sin, pos,
                                 inverse ? 1 : 0);
   return cudaGetLastError();
 }
@@ -262,6 +267,7 @@ __global__ void router_kernel(const float* __restrict__ logits, const float* __r
                               int score, int norm, float route_scale, float* __restrict__ w_out,
                               int* __restrict__ id_out, const float* __restrict__ bias_img,
                               const int* __restrict__ tok, int img_id) {
+  cb::pdl_entry();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= T) return;
   if (bias_img != nullptr && tok != nullptr && tok[warp] == img_id) bias = bias_img;
@@ -329,7 +335,7 @@ cudaError_t router_topk(const float* logits, const float* bias, int T, int E, in
   if (T == 0) return cudaSuccess;
   if (k > 32 || E > 1024) return cudaErrorInvalidValue;
   const int blocks = ceil_div(T * 32, 256);
-#define CB_ROUTER(N) router_kernel<N><<<blocks, 256, 0, s>>>(logits, bias, T, E, k, score, norm ? 1 : 0, route_scale, w, \
+#define CB_ROUTER(N) cb::launch_k(router_kernel<N>, blocks, 256, 0, s, logits, bias, T, E, k, score, norm ? 1 : 0, route_scale, w, \
                                                             ids, bias_img, tok, img_id)
   if (E <= 64) CB_ROUTER(2);
   else if (E <= 128) CB_ROUTER(4);
@@ -346,6 +352,7 @@ cudaError_t router_topk(const float* logits, const float* bias, int T, int E, in
 // CTA scans the padded counts and tags the blocks), scatter of (token, slot) pairs.  Row order inside an expert
 // segment is arbitrary (every row's GEMM result is independent of its position and the combine is per token).
 __global__ void moe_count_local_kernel(const int* __restrict__ ids, int Tk, int E, int* __restrict__ cnt) {
+  cb::pdl_entry();
   extern __shared__ int hcnt[];
   for (int e = threadIdx.x; e < E; e += blockDim.x) hcnt[e] = 0;
   __syncthreads();
@@ -361,6 +368,7 @@ __global__ void moe_count_local_kernel(const int* __restrict__ ids, int Tk, int 
 __global__ void moe_offsets_kernel(const int* __restrict__ cnt, int E, int align, int max_blocks,
                                    int* __restrict__ start, int* __restrict__ fill, int* __restrict__ m_block_expert,
                                    int* __restrict__ num_blocks, int* __restrict__ row_src) {
+  cb::pdl_entry();
   __shared__ int wsum[32];
   __shared__ int s_total;
   const int t = threadIdx.x, lane = t & 31, wid = t >> 5;
@@ -403,6 +411,7 @@ __global__ void moe_offsets_kernel(const int* __restrict__ cnt, int E, int align
 __global__ void moe_scatter_kernel(const int* __restrict__ ids, int Tk, int k, int E, const int* __restrict__ start,
                                    int* __restrict__ fill, int max_rows, int* __restrict__ slot_pos,
                                    int* __restrict__ row_src) {
+  cb::pdl_entry();
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < Tk; i += gridDim.x * blockDim.x) {
     const int e = ids[i];
     int pos = -1;
@@ -423,10 +432,10 @@ cudaError_t moe_layout(const int* ids, int T, int k, int E, int max_blocks, int*
   cudaError_t e = cudaMemsetAsync(counts, 0, sizeof(int) * E, s);
   if (e != cudaSuccess) return e;
   const int blocks = Tk / 1024 + 1 < 148 ? Tk / 1024 + 1 : 148;
-  moe_count_local_kernel<<<blocks, 256, E * sizeof(int), s>>>(ids, Tk, E, counts);
-  moe_offsets_kernel<<<1, 1024, 0, s>>>(counts, E, align, max_blocks, scratch, scratch + E, m_block_expert,
+  cb::launch_k(moe_count_local_kernel, blocks, 256, E * sizeof(int), s, ids, Tk, E, counts);
+  cb::launch_k(moe_offsets_kernel, 1, 1024, 0, s, counts, E, align, max_blocks, scratch, scratch + E, m_block_expert,
                                         num_blocks, row_src);
-  moe_scatter_kernel<<<blocks, 256, 0, s>>>(ids, Tk, k, E, scratch, scratch + E, max_blocks * 128, slot_pos,
+  cb::launch_k(moe_scatter_kernel, blocks, 256, 0, s, ids, Tk, k, E, scratch, scratch + E, max_blocks * 128, slot_pos,
                                             row_src);
   return cudaGetLastError();
 }
@@ -435,6 +444,7 @@ cudaError_t moe_layout(const int* ids, int T, int k, int E, int max_blocks, int*
 __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ Y, int ldy, const float* __restrict__ w,
                                    const int* __restrict__ slot_pos, int k, const __nv_bfloat16* __restrict__ add,
                                    __nv_bfloat16* __restrict__ out, int D) {
+  cb::pdl_entry();
   const int t = blockIdx.x;
   for (int c = threadIdx.x * 8; c < D; c += blockDim.x * 8) {
     float acc[8];
@@ -465,7 +475,7 @@ cudaError_t moe_combine(const void* Y, int ldy, const float* w, const int* slot_
                         void* out, int D, cudaStream_t s) {
   if (T == 0) return cudaSuccess;
   if (D % 8) return cudaErrorInvalidValue;
-  moe_combine_kernel<<<T, 128, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(Y), ldy, w, slot_pos, k,
+  cb::launch_k(moe_combine_kernel, T, 128, 0, s, reinterpret_cast<const __nv_bfloat16*>(Y), ldy, w, slot_pos, k,
                                        reinterpret_cast<const __nv_bfloat16*>(add),
                                        reinterpret_cast<__nv_bfloat16*>(out), D);
   return cudaGetLastError();
@@ -481,6 +491,7 @@ __global__ void mhc_coeffs_kernel(const float* __restrict__ mix, int ld_mix, con
                                   const float* __restrict__ base, const float* __restrict__ scale, int T, int flat_dim,
                                   int iters, float hc_eps, float rms_eps, float* __restrict__ pre,
                                   float* __restrict__ post, float* __restrict__ comb) {
+  cb::pdl_entry();
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= T) return;
   constexpr int HC = 4, NMIX = 24;
@@ -542,7 +553,7 @@ cudaError_t mhc_coeffs(const float* mix, int ld_mix, const float* sumsq, const f
                        int flat_dim, int iters, float hc_eps, float rms_eps, float* pre, float* post, float* comb,
                        cudaStream_t s) {
   if (T == 0) return cudaSuccess;
-  mhc_coeffs_kernel<<<ceil_div(T, 128), 128, 0, s>>>(mix, ld_mix, sumsq, base, scale, T, flat_dim, iters, hc_eps,
+  cb::launch_k(mhc_coeffs_kernel, ceil_div(T, 128), 128, 0, s, mix, ld_mix, sumsq, base, scale, T, flat_dim, iters, hc_eps,
                                                      rms_eps, pre, post, comb);
   return cudaGetLastError();
 }
@@ -551,6 +562,7 @@ cudaError_t mhc_coeffs(const float* mix, int ld_mix, const float* sumsq, const f
 __global__ void mhc_head_coeffs_kernel(const float* __restrict__ mix, int ld_mix, const float* __restrict__ sumsq,
                                        const float* __restrict__ base, const float* __restrict__ scale, int T,
                                        int flat_dim, float hc_eps, float rms_eps, float* __restrict__ pre) {
+  cb::pdl_entry();
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= T) return;
   const float rsq = rsqrtf(sumsq[t] / flat_dim + rms_eps);
@@ -561,7 +573,7 @@ __global__ void mhc_head_coeffs_kernel(const float* __restrict__ mix, int ld_mix
 cudaError_t mhc_head_coeffs(const float* mix, int ld_mix, const float* sumsq, const float* base, const float* scale,
                             int T, int flat_dim, float hc_eps, float rms_eps, float* pre, cudaStream_t s) {
   if (T == 0) return cudaSuccess;
-  mhc_head_coeffs_kernel<<<ceil_div(T, 128), 128, 0, s>>>(mix, ld_mix, sumsq, base, scale, T, flat_dim, hc_eps,
+  cb::launch_k(mhc_head_coeffs_kernel, ceil_div(T, 128), 128, 0, s, mix, ld_mix, sumsq, base, scale, T, flat_dim, hc_eps,
                                                           rms_eps, pre);
   return cudaGetLastError();
 }
@@ -573,6 +585,7 @@ __global__ void mhc_pre_norm_kernel(const __nv_bfloat16* __restrict__ X, const f
                                     const float* __restrict__ w, int D, float eps, __nv_bfloat16* __restrict__ y,
                                     uint8_t* __restrict__ q, uint32_t* __restrict__ sf, int row_blocks,
                                     const int* __restrict__ rows) {
+  cb::pdl_entry();
   __shared__ float red[32];
   const int t_out = blockIdx.x;
   const int t = rows ? rows[t_out] : t_out;
@@ -645,9 +658,9 @@ cudaError_t mhc_pre_norm(const void* X, const float* pre, const float* w, int T,
   auto XX = reinterpret_cast<const __nv_bfloat16*>(X);
   auto yy = reinterpret_cast<__nv_bfloat16*>(y);
   auto qq = reinterpret_cast<uint8_t*>(q);
-  if (per <= 1) mhc_pre_norm_kernel<1><<<T, 256, 0, s>>>(XX, pre, w, D, eps, yy, qq, sf, rb, rows);
-  else if (per <= 2) mhc_pre_norm_kernel<2><<<T, 256, 0, s>>>(XX, pre, w, D, eps, yy, qq, sf, rb, rows);
-  else if (per <= 4) mhc_pre_norm_kernel<4><<<T, 256, 0, s>>>(XX, pre, w, D, eps, yy, qq, sf, rb, rows);
+  if (per <= 1) cb::launch_k(mhc_pre_norm_kernel<1>, T, 256, 0, s, XX, pre, w, D, eps, yy, qq, sf, rb, rows);
+  else if (per <= 2) cb::launch_k(mhc_pre_norm_kernel<2>, T, 256, 0, s, XX, pre, w, D, eps, yy, qq, sf, rb, rows);
+  else if (per <= 4) cb::launch_k(mhc_pre_norm_kernel<4>, T, 256, 0, s, XX, pre, w, D, eps, yy, qq, sf, rb, rows);
   else return cudaErrorInvalidValue;
   return cudaGetLastError();
 }
@@ -657,6 +670,7 @@ cudaError_t mhc_pre_norm(const void* X, const float* pre, const float* w, int T,
 __global__ void mhc_post_mix_kernel(const __nv_bfloat16* X, const __nv_bfloat16* __restrict__ out,
                                     const float* __restrict__ post, const float* __restrict__ comb, int D,
                                     __nv_bfloat16* Xn, float* __restrict__ sumsq) {
+  cb::pdl_entry();
   __shared__ float red[32];
   const int t = blockIdx.x;
   float pst[4], cb[16];
@@ -702,7 +716,7 @@ cudaError_t mhc_post_mix(const void* X, const void* out, const float* post, cons
                          float* sumsq, cudaStream_t s) {
   if (T == 0) return cudaSuccess;
   if (D % 8) return cudaErrorInvalidValue;
-  mhc_post_mix_kernel<<<T, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(X),
+  cb::launch_k(mhc_post_mix_kernel, T, 256, 0, s, reinterpret_cast<const __nv_bfloat16*>(X),
                                         reinterpret_cast<const __nv_bfloat16*>(out), post, comb, D,
                                         reinterpret_cast<__nv_bfloat16*>(Xn), sumsq);
   return cudaGetLastError();
@@ -713,6 +727,7 @@ cudaError_t mhc_post_mix(const void* X, const void* out, const float* post, cons
 __global__ void embed_hc_kernel(const __nv_bfloat16* __restrict__ table, int row_lo, int rows,
                                 const int* __restrict__ ids, int D, int hc, __nv_bfloat16* __restrict__ X,
                                 float* __restrict__ sumsq) {
+  cb::pdl_entry();
   __shared__ float red[32];
   const int t = blockIdx.x;
   const int id = ids[t] - row_lo;
@@ -733,13 +748,14 @@ __global__ void embed_hc_kernel(const __nv_bfloat16* __restrict__ table, int row
 cudaError_t embed_hc(const void* table, int row_lo, int rows, const int* ids, int T, int D, int hc, void* X,
                      float* sumsq, cudaStream_t s) {
   if (T == 0) return cudaSuccess;
-  embed_hc_kernel<<<T, 128, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(table), row_lo, rows, ids, D, hc,
+  cb::launch_k(embed_hc_kernel, T, 128, 0, s, reinterpret_cast<const __nv_bfloat16*>(table), row_lo, rows, ids, D, hc,
                                     reinterpret_cast<__nv_bfloat16*>(X), sumsq);
   return cudaGetLastError();
 }
 
 // Row sum of squares of bf16 rows (length n): used where the producer of X did not emit it.
 __global__ void row_sumsq_kernel(const __nv_bfloat16* __restrict__ x, int64_t n, float* __restrict__ out) {
+  cb::pdl_entry();
   __shared__ float red[32];
   const int t = blockIdx.x;
   float ss = 0.f;
@@ -755,13 +771,14 @@ __global__ void row_sumsq_kernel(const __nv_bfloat16* __restrict__ x, int64_t n,
 cudaError_t row_sumsq(const void* x, int T, int64_t n, float* out, cudaStream_t s) {
   if (T == 0) return cudaSuccess;
   if (n % 8) return cudaErrorInvalidValue;
-  row_sumsq_kernel<<<T, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(x), n, out);
+  cb::launch_k(row_sumsq_kernel, T, 256, 0, s, reinterpret_cast<const __nv_bfloat16*>(x), n, out);
   return cudaGetLastError();
 }
 
 // SwiGLU on a bf16 [T, 2I] tensor whose halves are (gate | up) -> bf16 [T, I].
 __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int I, float limit,
                                 __nv_bfloat16* __restrict__ out) {
+  cb::pdl_entry();
   const int t = blockIdx.x;
   for (int c = threadIdx.x; c < I; c += blockDim.x) {
     float g = __bfloat162float(gu[size_t(t) * 2 * I + c]);
@@ -772,7 +789,7 @@ __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int I, flo
 }
 cudaError_t silu_mul(const void* gu, int T, int I, float limit, void* out, cudaStream_t s) {
   if (T == 0) return cudaSuccess;
-  silu_mul_kernel<<<T, 256, 0, s>>>(reinterpret_cast<const __nv_bfloat16*>(gu), I, limit,
+  cb::launch_k(silu_mul_kernel, T, 256, 0, s, reinterpret_cast<const __nv_bfloat16*>(gu), I, limit,
                                     reinterpret_cast<__nv_bfloat16*>(out));
   return cudaGetLastError();
 }

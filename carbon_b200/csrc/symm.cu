@@ -28,6 +28,7 @@ CB_DEVICE void red_release_sys_add(uint32_t* p, uint32_t v) {
 
 // One thread per peer: flag[peer][slot] = epoch, after all prior writes of this stream are visible system-wide.
 __global__ void signal_peers_kernel(const uint64_t* __restrict__ peer_flag_ptrs, int world, int slot, uint32_t epoch) {
+  cb::pdl_entry();
   __threadfence_system();
   const int r = threadIdx.x;
   if (r < world) st_release_sys(reinterpret_cast<uint32_t*>(peer_flag_ptrs[r]) + slot, epoch);
@@ -36,6 +37,7 @@ __global__ void signal_peers_kernel(const uint64_t* __restrict__ peer_flag_ptrs,
 // Wait until flags[0..world) >= epoch (wrap-safe comparison), bounded.
 __global__ void wait_flags_kernel(const uint32_t* __restrict__ flags, int world, uint32_t epoch, int* status,
                                   unsigned long long limit_ns) {
+  cb::pdl_entry();
   const int r = threadIdx.x;
   if (r >= world) return;
   const uint64_t t0 = globaltimer();
@@ -55,6 +57,7 @@ __global__ void wait_flags_kernel(const uint32_t* __restrict__ flags, int world,
 __global__ void p2p_barrier_kernel(const uint64_t* __restrict__ peer_flag_ptrs, int world, int my_rank,
                                    uint32_t* __restrict__ epoch_ctr, const uint32_t* __restrict__ my_flags,
                                    int* __restrict__ status, unsigned long long limit_ns) {
+  cb::pdl_entry();
   __shared__ uint32_t s_epoch;
   if (threadIdx.x == 0) {
     s_epoch = *epoch_ctr + 1u;
@@ -84,18 +87,18 @@ __global__ void p2p_barrier_kernel(const uint64_t* __restrict__ peer_flag_ptrs, 
 cudaError_t p2p_barrier(const uint64_t* peer_flag_ptrs, int world, int my_rank, uint32_t* epoch_ctr,
                         const uint32_t* my_flags, int* status, uint64_t limit_ns, cudaStream_t s) {
   if (world > 32) return cudaErrorInvalidValue;
-  p2p_barrier_kernel<<<1, 32, 0, s>>>(peer_flag_ptrs, world, my_rank, epoch_ctr, my_flags, status, limit_ns);
+  cb::launch_k(p2p_barrier_kernel, 1, 32, 0, s, peer_flag_ptrs, world, my_rank, epoch_ctr, my_flags, status, limit_ns);
   return cudaGetLastError();
 }
 
 cudaError_t signal_peers(const uint64_t* peer_flag_ptrs, int world, int slot, uint32_t epoch, cudaStream_t s) {
-  signal_peers_kernel<<<1, 32, 0, s>>>(peer_flag_ptrs, world, slot, epoch);
+  cb::launch_k(signal_peers_kernel, 1, 32, 0, s, peer_flag_ptrs, world, slot, epoch);
   return cudaGetLastError();
 }
 
 cudaError_t wait_flags(const uint32_t* flags, int world, uint32_t epoch, int* status, uint64_t limit_ns,
                        cudaStream_t s) {
-  wait_flags_kernel<<<1, 32, 0, s>>>(flags, world, epoch, status, limit_ns);
+  cb::launch_k(wait_flags_kernel, 1, 32, 0, s, flags, world, epoch, status, limit_ns);
   return cudaGetLastError();
 }
 

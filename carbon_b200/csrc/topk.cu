@@ -59,6 +59,7 @@ CB_DEVICE void select_digit(const int* hist, int* sw, uint32_t* s_prefix, int* s
 
 __global__ void topk_mask_kernel(const float* __restrict__ logits, int ldo, int Tq, int k, uint32_t* __restrict__ mask,
                                  int mask_words, int row0) {
+  cb::pdl_entry();
   extern __shared__ uint32_t vals[];
   __shared__ int hist[256];
   __shared__ int sw[32];
@@ -135,6 +136,7 @@ __global__ void topk_mask_kernel(const float* __restrict__ logits, int ldo, int 
 __global__ void topk_index_kernel(const float* __restrict__ logits, int ldo, const int* __restrict__ key_slots,
                                   int slot_stride, const int* __restrict__ n_keys, int row0, int Lmax, int k,
                                   int* __restrict__ out) {
+  cb::pdl_entry();
   extern __shared__ uint32_t vals[];
   __shared__ int hist[256];
   __shared__ int sw[32];
@@ -210,7 +212,7 @@ cudaError_t topk_slots(const float* logits, int ldo, const int* key_slots, int s
     cudaError_t e = smem_optin(topk_index_kernel, int(200 * 1024));
     if (e != cudaSuccess) return e;
   }
-  topk_index_kernel<<<T, 512, smem, s>>>(logits, ldo, key_slots, slot_stride, n_keys, row0, Lmax, k, out);
+  cb::launch_k(topk_index_kernel, T, 512, smem, s, logits, ldo, key_slots, slot_stride, n_keys, row0, Lmax, k, out);
   return cudaGetLastError();
 }
 
@@ -223,7 +225,7 @@ cudaError_t topk_mask(const float* logits, int ldo, int Tq, int k, uint32_t* mas
     cudaError_t e = smem_optin(topk_mask_kernel, int(200 * 1024));
     if (e != cudaSuccess) return e;
   }
-  topk_mask_kernel<<<Tq, 512, smem, s>>>(logits, ldo, Tq, k, mask, mask_words, row0);
+  cb::launch_k(topk_mask_kernel, Tq, 512, smem, s, logits, ldo, Tq, k, mask, mask_words, row0);
   return cudaGetLastError();
 }
 
