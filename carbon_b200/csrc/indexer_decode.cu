@@ -23,7 +23,7 @@ namespace idxd {
 
 constexpr int KT = 128;                 // keys per tile (MMA M)
 constexpr int DK = 128;                 // key / query dims (two 64-dim swizzle atoms)
-constexpr int STAGES = 3;
+constexpr int STAGES = 2;               // 84 KB of shared memory: two CTAs per SM (one wave for 32 x 4k keys)
 constexpr int TILES_PER_CTA = 4;
 constexpr int A_ATOM = KT * 128;        // 16 KB: 128 key rows x 64 dims
 constexpr int A_BYTES = 2 * A_ATOM;     // 32 KB per stage
@@ -103,15 +103,21 @@ __global__ void __launch_bounds__(192) indexer_decode_kernel(const __grid_consta
       tma_load_3d(sQ, &tm_q, q_full, 0, 0, t);
       tma_load_3d(sQ + q_atom, &tm_q, q_full, 64, 0, t);
     }
-    for (int j = 0; j < mma_tiles; ++j) {
-      const int s = j % STAGES;
-      int r[4];
+    // lane owns keys 4*lane .. 4*lane+3 of a tile; the next tile's slots are loaded one tile ahead
+    auto load_slots = [&](int j, int (&r)[4]) {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {                     // lane owns keys 4*lane .. 4*lane+3 of the tile
+      for (int i = 0; i < 4; ++i) {
         const int key = (tile0 + j) * KT + lane * 4 + i;
-        int slot = key < n ? __ldg(slots_t + key) : 0;
+        const int slot = (j < mma_tiles && key < n) ? __ldg(slots_t + key) : 0;
         r[i] = slot < 0 ? 0 : slot;                     // masked in the epilogue; keep the address valid
       }
+    };
+    int nxt[4];
+    load_slots(0, nxt);
+    for (int j = 0; j < mma_tiles; ++j) {
+      const int s = j % STAGES;
+      int r[4] = {nxt[0], nxt[1], nxt[2], nxt[3]};
+      load_slots(j + 1, nxt);
       int ok = 1;
       if (lane == 0) {
         ok = mbar_wait(&a_empty[s], ((j / STAGES) & 1) ^ 1) ? 1 : 0;
