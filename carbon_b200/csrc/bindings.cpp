@@ -91,14 +91,15 @@ void rope(torch::Tensor x, int64_t off, int64_t dim, torch::Tensor cos_sin, torc
 // bias_img / tok / img_id (optional): tokens with tok[t] == img_id rank with bias_img instead of bias
 void router_topk(torch::Tensor logits, c10::optional<torch::Tensor> bias, int64_t k, int64_t score, bool norm,
                  double route_scale, torch::Tensor w, torch::Tensor ids, c10::optional<torch::Tensor> bias_img,
-                 c10::optional<torch::Tensor> tok, int64_t img_id) {
+                 c10::optional<torch::Tensor> tok, int64_t img_id, int64_t n_groups, int64_t topk_groups) {
   CHECK_CUDA(logits); CHECK_DT(logits, at::kFloat); CHECK_CONTIG(logits);
   CHECK_DT(w, at::kFloat); CHECK_DT(ids, at::kInt);
   if (tok.has_value() && tok->defined()) { CHECK_DT((*tok), at::kInt); CHECK_CONTIG((*tok)); }
   c10::cuda::CUDAGuard g(logits.device());
   CK(cb::router_topk(logits.data_ptr<float>(), ptr_or_null<const float>(bias), logits.size(0), logits.size(1), k,
                      score, norm, float(route_scale), w.data_ptr<float>(), ids.data_ptr<int>(), cur_stream(),
-                     ptr_or_null<const float>(bias_img), ptr_or_null<const int>(tok), int(img_id)));
+                     ptr_or_null<const float>(bias_img), ptr_or_null<const int>(tok), int(img_id), int(n_groups),
+                     int(topk_groups)));
 }
 
 void moe_layout(torch::Tensor ids, int64_t E, torch::Tensor slot_pos, torch::Tensor row_src,

@@ -266,7 +266,7 @@ template <int EPL>  // experts per lane
 __global__ void router_kernel(const float* __restrict__ logits, const float* __restrict__ bias, int T, int E, int k,
                               int score, int norm, float route_scale, float* __restrict__ w_out,
                               int* __restrict__ id_out, const float* __restrict__ bias_img,
-                              const int* __restrict__ tok, int img_id) {
+                              const int* __restrict__ tok, int img_id, int n_groups, int topk_groups) {
   cb::pdl_entry();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (warp >= T) return;
@@ -301,6 +301,47 @@ __global__ void router_kernel(const float* __restrict__ logits, const float* __r
     const int e = i * 32 + lane;
     key[i] = e < E ? act[i] + (bias ? bias[e] : 0.f) : -INFINITY;
   }
+  if (n_groups > 1) {
+    // group-limited routing: keep the experts of the topk_groups groups whose two best keys sum highest (ties ->
+    // lower group id); group g holds experts [g*G, (g+1)*G)
+    const int G = E / n_groups;
+    float my_gs = -INFINITY;                 // lane g < n_groups: score of group g
+    for (int g = 0; g < n_groups; ++g) {
+      float b1 = -INFINITY, b2 = -INFINITY;  // this lane's two best keys in group g
+#pragma unroll
+      for (int i = 0; i < EPL; ++i) {
+        const int e = i * 32 + lane;
+        if (e < E && e / G == g) {
+          if (key[i] > b1) { b2 = b1; b1 = key[i]; } else if (key[i] > b2) { b2 = key[i]; }
+        }
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float o1 = __shfl_xor_sync(0xffffffffu, b1, o), o2 = __shfl_xor_sync(0xffffffffu, b2, o);
+        const float n1 = fmaxf(b1, o1);
+        const float n2 = fmaxf(fminf(b1, o1), fmaxf(b2, o2));
+        b1 = n1; b2 = n2;
+      }
+      if (lane == g) my_gs = b1 + b2;
+    }
+    uint32_t keep = 0;                       // bit g: group g selected
+    for (int r = 0; r < topk_groups; ++r) {
+      float bv = (lane < n_groups && !((keep >> lane) & 1u)) ? my_gs : -INFINITY;
+      int bi = lane < n_groups ? lane : 0x7fffffff;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+      }
+      if (bi < n_groups) keep |= 1u << bi;
+    }
+#pragma unroll
+    for (int i = 0; i < EPL; ++i) {
+      const int e = i * 32 + lane;
+      if (e < E && !((keep >> (e / G)) & 1u)) key[i] = -INFINITY;
+    }
+  }
   float wsum = 0.f, my_w = 0.f;
   int my_id = 0;
   for (int r = 0; r < k; ++r) {
@@ -331,12 +372,14 @@ __global__ void router_kernel(const float* __restrict__ logits, const float* __r
 }
 cudaError_t router_topk(const float* logits, const float* bias, int T, int E, int k, int score, bool norm,
                         float route_scale, float* w, int* ids, cudaStream_t s, const float* bias_img,
-                        const int* tok, int img_id) {
+                        const int* tok, int img_id, int n_groups, int topk_groups) {
   if (T == 0) return cudaSuccess;
   if (k > 32 || E > 1024) return cudaErrorInvalidValue;
+  if (n_groups > 1 && (n_groups > 32 || E % n_groups || topk_groups < 1 || topk_groups > n_groups))
+    return cudaErrorInvalidValue;
   const int blocks = ceil_div(T * 32, 256);
 #define CB_ROUTER(N) cb::launch_k(router_kernel<N>, blocks, 256, 0, s, logits, bias, T, E, k, score, norm ? 1 : 0, route_scale, w, \
-                                                            ids, bias_img, tok, img_id)
+                                                            ids, bias_img, tok, img_id, n_groups, topk_groups)
   if (E <= 64) CB_ROUTER(2);
   else if (E <= 128) CB_ROUTER(4);
   else if (E <= 256) CB_ROUTER(8);

@@ -16,9 +16,11 @@ cudaError_t rms_norm(const void* x, int ldx, const float* w, void* y, int ldy, v
 cudaError_t sf_pad(uint32_t* sf, int M, int K, cudaStream_t s);
 cudaError_t rope_inplace(void* x, int T, int64_t stride_t, int64_t stride_h, int H, int off, int dim,
                          const float* cos_sin, const int* pos, bool inverse, cudaStream_t s);
+// n_groups > 1: group-limited routing (experts only from the topk_groups groups with the best top-2 key sums)
 cudaError_t router_topk(const float* logits, const float* bias, int T, int E, int k, int score, bool norm,
                         float route_scale, float* w, int* ids, cudaStream_t s,
-                        const float* bias_img = nullptr, const int* tok = nullptr, int img_id = -1);
+                        const float* bias_img = nullptr, const int* tok = nullptr, int img_id = -1,
+                        int n_groups = 1, int topk_groups = 1);
 cudaError_t moe_layout(const int* ids, int T, int k, int E, int max_blocks, int* slot_pos, int* row_src,
                        int* m_block_expert, int* num_blocks, int* counts, cudaStream_t s, int align, int* scratch);
 cudaError_t moe_combine(const void* Y, int ldy, const float* w, const int* slot_pos, int T, int k, const void* add,

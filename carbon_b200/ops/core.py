@@ -73,8 +73,8 @@ def router_topk(logits: torch.Tensor, bias: Optional[torch.Tensor], k: int, scor
                 img_id: int = -1, n_groups: int = 1, topk_groups: int = 1) -> Tuple[torch.Tensor, torch.Tensor]:
     """Biased top-k router; with ``bias_img``, tokens whose id (``tok``) is ``img_id`` rank with that bias.
     Group-limited routing (``n_groups`` > 1: experts only from the ``topk_groups`` groups with the best top-2 key
-    sums) runs as tensor ops on the logits' device; the router kernel covers ungrouped routing."""
-    if not logits.is_cuda or n_groups > 1:
+    sums, ties toward the lower group) runs in the same kernel."""
+    if not logits.is_cuda:
         if bias_img is not None and tok is not None:
             is_img = (tok.long() == img_id)[:, None]
             b = bias if bias is not None else torch.zeros_like(bias_img)
@@ -85,7 +85,8 @@ def router_topk(logits: torch.Tensor, bias: Optional[torch.Tensor], k: int, scor
     w = torch.empty(T, k, dtype=torch.float32, device=logits.device)
     ids = torch.empty(T, k, dtype=torch.int32, device=logits.device)
     ext().router_topk(logits.float().contiguous(), bias, k, SCORE_FUNCS[score_func], norm, float(route_scale), w, ids,
-                      bias_img, tok.to(torch.int32).contiguous() if tok is not None else None, int(img_id))
+                      bias_img, tok.to(torch.int32).contiguous() if tok is not None else None, int(img_id),
+                      int(n_groups), int(topk_groups))
     return w, ids
 
 

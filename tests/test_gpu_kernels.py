@@ -221,6 +221,21 @@ def test_router_topk(score, E, k):
     assert rel_err(w, w_ref) < 1e-5
 
 
+@pytest.mark.parametrize("E,k,ng,tg", [(256, 8, 8, 4), (64, 6, 4, 2), (160, 6, 5, 3)])
+def test_router_group_limited(E, k, ng, tg):
+    """Group-limited routing (DeepSeek-V3: 8 groups, the 4 best by their top-2 sum) in the router kernel."""
+    from carbon_b200.ops.core import router_topk
+
+    torch.manual_seed(4)
+    T = 211
+    logits = torch.randn(T, E)
+    bias = torch.randn(E) * 0.5
+    w, ids = router_topk(logits.to(DEV), bias.to(DEV), k, "sigmoid", 2.5, True, n_groups=ng, topk_groups=tg)
+    w_ref, ids_ref = R.router_topk(logits, bias, k, "sigmoid", 2.5, True, ng, tg)
+    assert torch.equal(ids.cpu(), ids_ref)
+    assert rel_err(w, w_ref) < 1e-5
+
+
 def test_router_ties_prefer_lower_id():
     from carbon_b200.ops.core import router_topk
 
