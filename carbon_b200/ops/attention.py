@@ -65,10 +65,29 @@ def mla_prefill(q: torch.Tensor, kvb: torch.Tensor, kpe: torch.Tensor, cu_seqlen
     if version == 0:
         version = 3 if mask is not None else 2
     out = torch.empty(T, H, 128, dtype=torch.bfloat16, device=q.device)
-    tiles = prefill_tiles(cu_seqlens, 256 if version >= 2 else 128).to(q.device, non_blocking=True)
+    tiles = _device_tiles(cu_seqlens, 256 if version >= 2 else 128, q.device)
     ext().attn_prefill(q.contiguous(), kvb.contiguous(), kpe.contiguous(), tiles, mask, float(scale), out, None,
                        version, trace, sink.float().contiguous() if sink is not None else None)
     return out
+
+
+_TILES = {}
+
+
+def _device_tiles(cu_seqlens: List[int], bm: int, device) -> torch.Tensor:
+    """``prefill_tiles`` on the device, cached by batch layout: every layer of a forward reuses one copy, and the
+    first copy goes through pinned memory, so no layer waits on the host for a pageable transfer."""
+    key = (tuple(cu_seqlens), bm, str(device))
+    t = _TILES.get(key)
+    if t is None:
+        if len(_TILES) > 64:
+            _TILES.clear()
+        host = prefill_tiles(cu_seqlens, bm)
+        if torch.cuda.is_available():
+            host = host.pin_memory()
+        t = host.to(device, non_blocking=True)
+        _TILES[key] = t
+    return t
 
 
 def prefill_tiles(cu_seqlens: List[int], bm: int = 128) -> torch.Tensor:
