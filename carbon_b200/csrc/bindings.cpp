@@ -372,6 +372,15 @@ void engram_gate(torch::Tensor X, torch::Tensor kv, torch::Tensor qw, torch::Ten
 }
 
 // decode-side DSA: q [T, H, 128] bf16, w [T, H] fp32, kc [S, 128] bf16, key_slots [T, L], n_keys [T] -> out [T, k]
+void mhc_stats_small(torch::Tensor X, torch::Tensor fn, int64_t rows, torch::Tensor out) {
+  CHECK_CUDA(X); CHECK_DT(X, at::kBFloat16); CHECK_DT(fn, at::kBFloat16); CHECK_DT(out, at::kFloat);
+  CHECK_CONTIG(fn); TORCH_CHECK(X.dim() == 2 && X.stride(1) == 1 && out.stride(1) == 1);
+  TORCH_CHECK(fn.size(1) == X.size(1) && rows <= fn.size(0) && out.size(1) >= rows && out.size(0) == X.size(0));
+  c10::cuda::CUDAGuard g(X.device());
+  CK(cb::mhc_stats_small(X.data_ptr(), X.stride(0), fn.data_ptr(), int(rows), X.size(1), X.size(0),
+                         out.data_ptr<float>(), out.stride(0), cur_stream()));
+}
+
 void indexer_decode_logits(torch::Tensor q, torch::Tensor w, torch::Tensor kc, torch::Tensor key_slots,
                            torch::Tensor n_keys, torch::Tensor logits) {
   CHECK_CUDA(q); CHECK_CONTIG(q); CHECK_CONTIG(kc); CHECK_CONTIG(key_slots); CHECK_CONTIG(logits);
@@ -445,4 +454,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("indexer_topk", &indexer_topk);
   m.def("indexer_decode_logits", &indexer_decode_logits);
   m.def("topk_causal_slots", &topk_causal_slots);
+  m.def("mhc_stats_small", &mhc_stats_small);
 }

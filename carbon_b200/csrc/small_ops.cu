@@ -592,6 +592,55 @@ __global__ void mhc_coeffs_kernel(const float* __restrict__ mix, int ld_mix, con
 #pragma unroll
     for (int o = 0; o < HC; ++o) comb[t * 16 + i * HC + o] = c[i][o];
 }
+// mHC mixing statistics for few tokens (decode): mix[t, r] = Σ_k X[t, k] · fn[r, k] for the fn rows r < R (bf16
+// [hi; lo] parts of the fp32 projections), fp32 accumulation.  One CTA per (token, 8 fn rows): each thread walks
+// 8-column chunks of the row (16-byte loads of X and of the 8 fn rows), then a block reduction per output.  The
+// tensor-core GEMM would run a single 128-row tile split over K for a decode batch.
+__global__ void __launch_bounds__(256) mhc_stats_small_kernel(const __nv_bfloat16* __restrict__ X, int ldx,
+                                                               const __nv_bfloat16* __restrict__ fn, int K,
+                                                               float* __restrict__ out, int ldo) {
+  cb::pdl_entry();
+  __shared__ float red[8][8];
+  const int t = blockIdx.x, r0 = blockIdx.y * 8;
+  const __nv_bfloat16* xr = X + size_t(t) * ldx;
+  float acc[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) acc[r] = 0.f;
+  for (int c = threadIdx.x * 8; c < K; c += blockDim.x * 8) {
+    const uint4 xv = *reinterpret_cast<const uint4*>(xr + c);
+    const float x[8] = {bf16_lo(xv.x), bf16_hi(xv.x), bf16_lo(xv.y), bf16_hi(xv.y),
+                        bf16_lo(xv.z), bf16_hi(xv.z), bf16_lo(xv.w), bf16_hi(xv.w)};
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const uint4 fv = __ldg(reinterpret_cast<const uint4*>(fn + size_t(r0 + r) * K + c));
+      acc[r] += x[0] * bf16_lo(fv.x) + x[1] * bf16_hi(fv.x) + x[2] * bf16_lo(fv.y) + x[3] * bf16_hi(fv.y) +
+                x[4] * bf16_lo(fv.z) + x[5] * bf16_hi(fv.z) + x[6] * bf16_lo(fv.w) + x[7] * bf16_hi(fv.w);
+    }
+  }
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    const float v = warp_sum(acc[r]);
+    if (lane == 0) red[wid][r] = v;
+  }
+  __syncthreads();
+  if (threadIdx.x < 8) {
+    float v = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) v += red[w][threadIdx.x];
+    out[size_t(t) * ldo + r0 + threadIdx.x] = v;
+  }
+}
+
+cudaError_t mhc_stats_small(const void* X, int ldx, const void* fn, int R, int K, int T, float* out, int ldo,
+                            cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  if (R % 8 || K % 8 || ldx % 8) return cudaErrorInvalidValue;
+  cb::launch_k(mhc_stats_small_kernel, dim3(T, R / 8), 256, 0, s, reinterpret_cast<const __nv_bfloat16*>(X), ldx,
+               reinterpret_cast<const __nv_bfloat16*>(fn), K, out, ldo);
+  return cudaGetLastError();
+}
+
 cudaError_t mhc_coeffs(const float* mix, int ld_mix, const float* sumsq, const float* base, const float* scale, int T,
                        int flat_dim, int iters, float hc_eps, float rms_eps, float* pre, float* post, float* comb,
                        cudaStream_t s) {

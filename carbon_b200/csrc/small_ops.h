@@ -25,6 +25,9 @@ cudaError_t moe_layout(const int* ids, int T, int k, int E, int max_blocks, int*
                        int* m_block_expert, int* num_blocks, int* counts, cudaStream_t s, int align, int* scratch);
 cudaError_t moe_combine(const void* Y, int ldy, const float* w, const int* slot_pos, int T, int k, const void* add,
                         void* out, int D, cudaStream_t s);
+// mHC statistics for few tokens: mix[t, r] = X[t] · fn[r] for r < R, fp32 (CUDA cores; decode batches)
+cudaError_t mhc_stats_small(const void* X, int ldx, const void* fn, int R, int K, int T, float* out, int ldo,
+                            cudaStream_t s);
 cudaError_t mhc_coeffs(const float* mix, int ld_mix, const float* sumsq, const float* base, const float* scale, int T,
                        int flat_dim, int iters, float hc_eps, float rms_eps, float* pre, float* post, float* comb,
                        cudaStream_t s);

@@ -379,7 +379,7 @@ class DeepseekModel:
             return R.mhc_coeffs(X, hp.fn, hp.base, hp.scale, cfg.hc_mult, cfg.sinkhorn_iters, cfg.hc_eps, cfg.rms_eps)
         from ..ops._ext import ext
 
-        mix = bf16_gemm(X.view(T, X.shape[1] * X.shape[2]), hp.fn, out_dtype=torch.float32)
+        mix = mhc_mix(X.view(T, X.shape[1] * X.shape[2]), hp.fn)
         pre = torch.empty(T, 4, device=X.device)
         post = torch.empty(T, 4, device=X.device)
         comb = torch.empty(T, 4, 4, device=X.device)
@@ -968,7 +968,7 @@ class DeepseekModel:
             T = X.shape[0]
             pre = torch.empty(T, 4, device=X.device)
             if T > 0:
-                mix = bf16_gemm(X.view(T, X.shape[1] * X.shape[2]), self.head_hc.fn, out_dtype=torch.float32)
+                mix = mhc_mix(X.view(T, X.shape[1] * X.shape[2]), self.head_hc.fn)
                 ext().mhc_head_coeffs(mix, sumsq, self.head_hc.base, self.head_hc.scale, X.shape[1] * X.shape[2],
                                       cfg.hc_eps, cfg.rms_eps, pre)
             y, _ = self.pre_norm(X, pre, self.norm_w, want_fp8=False)
@@ -977,6 +977,20 @@ class DeepseekModel:
         if not self.on_gpu and pc.world == 1:
             return y @ self.head_w.w.t()
         return pc.lm_head(self, y)
+
+
+def mhc_mix(x: torch.Tensor, fn: torch.Tensor) -> torch.Tensor:
+    """mHC statistics x · fnᵀ (fp32 [T, rows of fn]) on the GPU: the tensor-core GEMM for prefill-sized batches, a
+    CUDA-core kernel with one CTA per (token, 8 rows) for decode-sized ones (a GEMM would run one tile split over
+    the 28k-long K)."""
+    T = x.shape[0]
+    if T <= 64:
+        from ..ops._ext import ext
+
+        out = torch.empty(T, fn.shape[0], dtype=torch.float32, device=x.device)
+        ext().mhc_stats_small(x, fn, fn.shape[0], out)
+        return out
+    return bf16_gemm(x, fn, out_dtype=torch.float32)
 
 
 def head_bmm(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:

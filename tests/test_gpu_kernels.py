@@ -292,6 +292,17 @@ def test_mhc_kernels():
     assert rel_err(ss2, Xn.float().pow(2).sum((1, 2))) < 1e-4
 
 
+@pytest.mark.parametrize("T,rows", [(1, 48), (32, 48), (64, 16)])
+def test_mhc_stats_small_matches_fp32(T, rows):
+    """Decode-sized mHC statistics (CUDA-core kernel) against fp32 math on the same bf16 inputs."""
+    K = 4 * 7168
+    X = torch.randn(T, K).to(torch.bfloat16)
+    fn = (torch.randn(rows, K) * 0.02).to(torch.bfloat16)
+    out = torch.empty(T, rows, device=DEV)
+    _ext().mhc_stats_small(X.to(DEV), fn.to(DEV), rows, out)
+    assert rel_err(out, X.float() @ fn.float().t()) < 1e-5
+
+
 # ----------------------------------------------------------------------------------------------------------------------
 # attention
 # ----------------------------------------------------------------------------------------------------------------------
