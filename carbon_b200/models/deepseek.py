@@ -291,6 +291,12 @@ class DeepseekModel:
         else:
             L.wq = Lin(get(a + "wq.weight", slice(h0 * dq, h1 * dq)), dev, self.fp8)
         L.wkv_a = Lin(get(a + "wkv_a.weight"), dev, self.fp8)
+        L.wqkv_a = None
+        if self.on_gpu and cfg.q_lora_rank > 0 and L.wq_a.kind == "fp8" and L.wkv_a.kind == "fp8":
+            # both down-projections read the same normalised input: one GEMM over the stacked weights (the output
+            # columns [0, q_lora) feed the query path, the rest is the KV latent)
+            L.wqkv_a = Lin(torch.cat([get(a + "wq_a.weight"), get(a + "wkv_a.weight")]), dev, self.fp8)
+            L.wq_a = L.wkv_a = None
         L.kv_norm = get(a + "kv_norm.weight")
         L.wkv_b = None
         if cfg.attn_kind == "mla":
@@ -436,15 +442,19 @@ class DeepseekModel:
         lo, hi = pc.local
         pos_l = fb.pos[lo:hi]
         dp = pc.attn_dp and pc.world > 1         # attention over this rank's own sequences, all heads
+        qkv = None
+        if L.wqkv_a is not None:
+            with region("attn.q_proj"):
+                qkv = L.wqkv_a(h, xq=hq)                                        # [T_l, q_lora + latent_dim]
         with region("attn.q_proj"):
             if cfg.q_lora_rank > 0:
-                q_lat_raw = L.wq_a(h, xq=hq)
+                q_lat_raw = qkv[:, :cfg.q_lora_rank] if qkv is not None else L.wq_a(h, xq=hq)
                 q_lat_l = C.rms_norm(q_lat_raw, L.q_norm, cfg.rms_eps) if self.on_gpu else \
                     R.rms_norm(q_lat_raw, L.q_norm, cfg.rms_eps)
             else:
                 q_lat_l = h
         with region("attn.kv_proj"):
-            kv = L.wkv_a(h, xq=hq)                                                  # [T_l, latent_dim]
+            kv = qkv[:, cfg.q_lora_rank:] if qkv is not None else L.wkv_a(h, xq=hq)   # [T_l, latent_dim]
             if cfg.attn_kind == "latent_mqa":
                 # the shared KV head: the normalised latent with RoPE on its last dr dims
                 kv_c = C.rms_norm(kv.contiguous(), L.kv_norm, cfg.rms_eps) if self.on_gpu else \
