@@ -145,6 +145,15 @@ inline cudaError_t smem_optin(F* fn, int bytes) {
   return smem_optin(reinterpret_cast<const void*>(fn), bytes);
 }
 
+// End of a kernel that stored into peer GPUs' memory: one system-scope fence per CTA instead of one per thread.
+// The block barrier orders every thread's stores before thread 0's fence (fences are cumulative over what the
+// fencing thread has observed), and the kernel's completion orders that fence before the next kernel's barrier
+// release that lets the peers read.  Every thread of the block must call it (it contains __syncthreads).
+CB_DEVICE void publish_peer_stores() {
+  __syncthreads();
+  if (threadIdx.x == 0) __threadfence_system();
+}
+
 // Programmatic dependent launch.  Every kernel of this library starts with pdl_entry(): it waits until the kernel
 // launched before it in the stream has completed and its memory is visible (a no-op when this launch carries no
 // programmatic dependency), then lets the next kernel of the stream be launched early, so that its launch and

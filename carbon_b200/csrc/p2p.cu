@@ -35,7 +35,7 @@ __global__ void p2p_gather_kernel(const uint8_t* __restrict__ src, int n, int ro
       reinterpret_cast<V*>(dst)[c] = v;
     }
   }
-  __threadfence_system();   // this thread's peer stores are performed before any later barrier publishes them
+  publish_peer_stores();    // the peer stores are performed before any later barrier publishes them
 }
 
 cudaError_t p2p_gather_rows(const void* src, int n, int row_bytes, const uint64_t* dst_ptrs, int world, int row0,
@@ -82,7 +82,7 @@ __global__ void p2p_a2a_heads_kernel(const uint8_t* __restrict__ src, const int*
   }
   for (int c = threadIdx.x; c < C / 16; c += blockDim.x)
     reinterpret_cast<uint4*>(t)[c] = reinterpret_cast<const uint4*>(s)[c];
-  __threadfence_system();
+  publish_peer_stores();
 }
 
 cudaError_t p2p_a2a_heads(const void* src, const int* bounds_dev, int world, int my_rank, const uint64_t* dst_ptrs,
@@ -113,7 +113,7 @@ __global__ void p2p_scatter_kernel(const __nv_bfloat16* __restrict__ part, int D
     __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(slot_ptrs[r]) + (size_t(my_rank) * slot_rows + li) * D;
     reinterpret_cast<uint4*>(dst)[c] = v;
   }
-  __threadfence_system();
+  publish_peer_stores();
 }
 
 __global__ void reduce_slots_kernel(const __nv_bfloat16* __restrict__ slots, int world, int slot_rows, int n, int D,
@@ -327,7 +327,7 @@ __global__ void moe_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int D, 
                     (size_t(g) * row_blocks + rb) * 128 + (r & 31) * 4 + (r >> 5);
     *sfw = s_sf[g];
   }
-  __threadfence_system();
+  publish_peer_stores();
 }
 
 cudaError_t moe_dispatch(const void* x, int T, int D, const int* ids, int k, int El, int my_rank,
