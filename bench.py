@@ -56,6 +56,8 @@ def parse():
                          "(a2a) or row-parallel projection + reduce-scatter (rs)")
     ap.add_argument("--replicated-kv", action="store_true",
                     help="N>1: every rank caches every request's KV (default: only each request's home rank does)")
+    ap.add_argument("--kv", default="fp8", choices=["fp8", "bf16"],
+                    help="latent KV cache format (fp8: 656 bytes per token and layer, bf16: 1152)")
     ap.add_argument("--attn", default="tp", choices=["tp", "dp"],
                     help="attention parallelism for N>1: tensor-parallel over heads (the headline configuration) or "
                          "data-parallel over each rank's own sequences")
@@ -156,7 +158,7 @@ def main():
 
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180), device_id=dev)
     ext()
-    cfg = PRESETS[args.config]()
+    cfg = PRESETS[args.config]().replace(kv_fp8=args.kv == "fp8")
     if args.layers:
         cfg = cfg.replace(n_layers=args.layers)
     P, S = args.prompts_per_gpu, args.prompt_len
@@ -348,6 +350,8 @@ def main():
                        "weights": (f"{sets} distinct MoE-layer weight sets cycled over {n_moe} MoE layers "
                                    "(every layer still runs; the full untied model needs 8 GPUs)") if tied
                        else "all layers distinct", "l2": "inputs (weights) larger than L2",
+                       "kv_cache": "fp8 e4m3 latent rows, UE8M0 per 64 dims + fp16 RoPE key (656 B/token/layer)"
+                       if cfg.kv_fp8 else "bf16 latent rows (1152 B/token/layer)",
                        "init_s": round(init_s, 1)},
         }
         print(json.dumps(line), flush=True)
@@ -421,7 +425,11 @@ def roofline(cfg, world: int, prompts_per_gpu: int, seq: int, decode_per_gpu: in
     touched = El * (1 - (1 - 1 / E) ** (B_tot * k)) if E else 0
     wbytes = n_moe * (touched * expert + cfg.n_shared_experts * expert) + L * attn_w / world + \
         n_dense * 3 * D * cfg.dense_intermediate + n_idx * idx_w * 2
-    kv = decode_per_gpu * (L * min(ctx, topk) * cfg.latent_dim * 2 + n_idx * ctx * cfg.index_head_dim * 2)
+    from carbon_b200.ref import ops as R
+
+    row = R.latent_fp8_row_bytes(cfg.kv_lora_rank, cfg.qk_rope_head_dim, cfg.attn_kind == "mla") if cfg.kv_fp8 \
+        else cfg.latent_dim * 2
+    kv = decode_per_gpu * (L * min(ctx, topk) * row + n_idx * ctx * cfg.index_head_dim * 2)
     t_dec = (wbytes + kv) / (peak["hbm_gbs"] * 1e9)
     return {"prefill_frac": round(t_pf / (prefill_ms / 1e3), 3), "decode_frac": round(t_dec / (decode_ms / 1e3), 3),
             "prefill_tflop_per_gpu_step": round((fp8_flops + bf16_flops) / 1e12, 1),

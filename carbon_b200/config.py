@@ -57,6 +57,10 @@ class ModelConfig:
     # indexer q and k in fp8 e4m3 with one UE8M0 scale per 128-dim row (per head for q), the DeepSeek-V3.2 indexer
     # precision: the prefill logits run as block-scaled fp8 tcgen05 MMAs; decode sees the same rounded values
     index_fp8: bool = False
+    # latent KV cache in fp8: per token, the kv_lora_rank latent values in e4m3 with one UE8M0 scale per 64-dim atom
+    # and (MLA) the RoPE key in fp16 -- 656 bytes per MLA token instead of 1152 in bf16, 528 per latent-MQA token
+    # instead of 1024 (the reference's fp8 SWA pages: king_v10/bundle_v9/cuda_prefill_attn.py:2312-2340)
+    kv_fp8: bool = False
     # MLA prefill over sequences longer than this runs as absorbed sparse attention over each query's top-k cached
     # latent rows (cost linear in length at a fixed top-k) instead of the dense causal kernel with a DSA key mask
     # (cheaper for short prompts: 320 vs 1088 MACs per key and head); 0 = always the dense kernel

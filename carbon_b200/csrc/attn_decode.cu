@@ -16,6 +16,7 @@
 // Reference kernels with the same role: FlashMLA-derived decode / verify attention over the paged latent cache
 // (king_v10/bundle_v9/dec/cuda_decode_attn.py:20-116, dec/cuda_vattn.py:4654).
 #include <cudaTypedefs.h>
+#include <cuda_fp16.h>
 #include "ptx.cuh"
 
 namespace cb {
@@ -26,21 +27,32 @@ constexpr int HM = 128;                // head rows per CTA (M)
 // last 64 dims carry RoPE).  The value is always the first DL = 512 dims of the row.
 constexpr int DL = 512, DHALF = 256;
 constexpr int KT = 32;                 // keys per tile (N of Q·Kᵀ, K of P·V)
-constexpr int STAGES = 5;
 constexpr int NAC_MAX = 5;             // atoms one CTA of the pair owns (value half + the RoPE atom)
 constexpr int Q_ATOM = HM * 128;       // 16 KB: 128 rows x 64 dims
 constexpr int KV_ATOM = KT * 128;      // 4 KB: 32 rows x 64 dims
+// bf16 rows: the gathered atoms go straight into 5 operand stages
+constexpr int STAGES = 5;
 constexpr int KV_STAGE = NAC_MAX * KV_ATOM;
+// fp8 rows: TMA gathers raw row pieces into 4 staging slots; two converter warps expand the value atoms to fp16
+// operand tiles (3 stages).  A slot holds the RoPE atom (fp16, already in the 128B-swizzled operand layout, read by
+// the MMA in place), the CTA's 256 value bytes of every row (two 128-byte boxes) and the 16 scale bytes of every row
+// (one 4-row gather per 128-byte line: row r at F8_SC + (r / 4) * 128 + (r % 4) * 16).
+constexpr int F8_SLOTS = 4, F8_STAGES = 3;
+constexpr int F8_KV_STAGE = 4 * KV_ATOM;
+constexpr int F8_PE = 0, F8_VAL = 4096, F8_SC = 12288, F8_SLOT = 13312;
+constexpr int F8_SC_BOX = 16;
 // one partial-score exchange buffer: 128 rows x 32 fp32, rows padded to 36 floats so that the eight threads of a
 // quarter warp reading 16 bytes of eight consecutive rows hit eight different 4-bank groups
 constexpr int X_LD = KT + 4;
 constexpr int X_BYTES = HM * X_LD * 4;
 // TMEM: O [128 x 256] fp32 at columns [0, 256); two S buffers of 64 columns at 256 and 320 (P overwrites the first
-// KT/2 columns of its S buffer as packed bf16 and is read there by the P·V MMA)
+// KT/2 columns of its S buffer as packed 16-bit values and is read there by the P·V MMA)
 constexpr int TM_O = 0, TM_S = 256, TM_S_STRIDE = 64;
-constexpr int SMEM = 1024 + NAC_MAX * Q_ATOM + STAGES * KV_STAGE + 2 * X_BYTES + 256;
-template <int NA>
-constexpr int smem_bytes() { return SMEM; }
+template <bool F8>
+constexpr int smem_bytes() {
+  return 1024 + NAC_MAX * Q_ATOM + (F8 ? F8_STAGES * F8_KV_STAGE + F8_SLOTS * F8_SLOT : STAGES * KV_STAGE) +
+         2 * X_BYTES + 256;
+}
 constexpr float kRescaleThresh = 8.0f;
 
 struct Params {
@@ -71,48 +83,73 @@ CB_DEVICE void tma_gather4(void* dst, const void* tmap, uint64_t* bar, int col, 
       : "memory");
 }
 
+// Two e4m3 values (low byte first) -> two fp16 (exact conversion).
+CB_DEVICE uint32_t e4m3x2_to_f16x2(uint32_t v) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(uint16_t(v)));
+  return r;
+}
+CB_DEVICE uint32_t hmul2_u32(uint32_t a, uint32_t s) {
+  uint32_t r;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(s));
+  return r;
+}
+CB_DEVICE uint32_t pack_f16x2(float a, float b) {
+  __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
 // Global atom index of local atom `la` in CTA `hh` of the pair: the CTA's value half (atoms 4hh .. 4hh+3) first,
 // then (MLA rows, CTA 0) the RoPE-key atom 8.
 CB_DEVICE int atom_of(int hh, int la) { return la < 4 ? hh * 4 + la : 8; }
 
 // One token's keys [split*chunk, ...) are handled by a cluster of two CTAs (blockIdx.y = cluster rank hh).  The row
 // of a cached key is split between them by 64-dim atoms: CTA hh gathers only its value half (and CTA 0 the RoPE
-// atom), so no byte of a key row is read twice, and a CTA keeps 5 tiles of 32 keys in flight.  Each CTA computes the
-// partial S over its atoms; the two partials are exchanged through distributed shared memory every tile, so both
-// CTAs hold the same S and the same softmax (addition is commutative: identical m, l and P), and each accumulates
-// P·V for its own value half.
-//   TMA   Q atoms once; the CTA's atoms of KV tile j into stage j % 5 after P·V(j-5) released it
+// atom), so no byte of a key row is read twice.  Each CTA computes the partial S over its atoms; the two partials
+// are exchanged through distributed shared memory every tile, so both CTAs hold the same S and the same softmax
+// (addition is commutative: identical m, l and P), and each accumulates P·V for its own value half.
+//   TMA   Q atoms once; then per 32-key tile the CTA's pieces of the gathered rows (bf16: into operand stage j % 5
+//         once P·V(j-5) released it; fp8: into staging slot j % 4 once its conversion and Q·Kᵀ(j-4) are done)
+//   CVT   (fp8 rows, warps 2-3) staging slot j % 4 -> fp16 value atoms of operand stage j % 3, scaled per atom
 //   MMA   QK(0) QK(1) | PV(0) QK(2) | PV(1) QK(3) | ...   S(j) goes to buffer j % 2; PV(j) reads P(j) from the same
 //         columns and QK(j+2) overwrites them afterwards (tcgen05 MMAs of one thread execute in issue order)
 //   softmax (one head row per thread): partial S -> peer's exchange buffer, peer's partial + own = S, online
 //         softmax with lazy O rescale (only when the running max grows by more than 2^8), P over S in TMEM
-template <int NA>
+// fp8 rows run the MMAs in fp16 (q arrives as fp16; fp16 holds every e4m3 value times its power-of-two scale).
+template <int NA, bool F8>
 __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constant__ CUtensorMap tm_q,
                                                             const __grid_constant__ CUtensorMap tm_kv,
+                                                            const __grid_constant__ CUtensorMap tm_sc,
+                                                            const __grid_constant__ CUtensorMap tm_pe,
                                                             const Params p) {
   cb::pdl_entry();
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 1000
+  constexpr int NST = F8 ? F8_STAGES : STAGES;               // operand stages
+  constexpr int STAGE_B = F8 ? F8_KV_STAGE : KV_STAGE;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sKV = sQ + NAC_MAX * Q_ATOM;
-  float* xbuf = reinterpret_cast<float*>(sKV + STAGES * KV_STAGE);   // [2][128][X_LD]: the PEER's partial S
+  uint8_t* sST = sKV + NST * STAGE_B;                         // fp8 staging slots
+  float* xbuf = reinterpret_cast<float*>(sST + (F8 ? F8_SLOTS * F8_SLOT : 0));   // [2][128][X_LD]: the PEER's partial S
   uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(xbuf) + 2 * X_BYTES);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;              // [STAGES]
-  uint64_t* kv_empty = kv_full + STAGES;     // [STAGES]
-  uint64_t* s_full = kv_empty + STAGES;      // [2]
+  uint64_t* kv_full = bars + 1;              // [NST]
+  uint64_t* kv_empty = kv_full + NST;        // [NST]
+  uint64_t* s_full = kv_empty + NST;         // [2]
   uint64_t* p_full = s_full + 2;             // [2]
   uint64_t* pv_done = p_full + 2;            // [2]: PV(j) completes phase j >> 1 of pv_done[j & 1]
   uint64_t* x_full = pv_done + 2;            // [2]: the peer's partial of tile j landed in xbuf[j & 1] (tx bytes)
   uint64_t* x_empty = x_full + 2;            // [2]: the peer consumed this CTA's partial of tile j
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(x_empty + 2);
+  uint64_t* st_full = x_empty + 2;           // [F8_SLOTS] fp8: a slot's gathers landed (tx bytes)
+  uint64_t* st_empty = st_full + F8_SLOTS;   // [F8_SLOTS] fp8: both converter warps and Q·Kᵀ are done with a slot
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(st_empty + F8_SLOTS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int t = blockIdx.x, hh = int(cluster_ctarank()), split = blockIdx.z;
   const uint32_t peer = uint32_t(hh ^ 1);
-  const int nac = (NA == 9 && hh == 0) ? 5 : 4;
-  const int kv_bytes = nac * KV_ATOM;
+  const bool rope = NA == 9 && hh == 0;      // this CTA owns the RoPE-key atom
+  const int nac = rope ? 5 : 4;
   const int k_begin = split * p.chunk;
   const int k_end = min(p.K, k_begin + p.chunk);
   const int n_tiles = k_end > k_begin ? (k_end - k_begin + KT - 1) / KT : 0;   // the same in both CTAs
@@ -121,11 +158,13 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < STAGES; ++i) { mbar_init(&kv_full[i], 1); mbar_init(&kv_empty[i], 1); }
+    for (int i = 0; i < NST; ++i) { mbar_init(&kv_full[i], F8 ? 2 : 1); mbar_init(&kv_empty[i], 1); }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1); mbar_init(&p_full[i], 128); mbar_init(&pv_done[i], 1);
       mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], 128);
     }
+    if (F8)
+      for (int i = 0; i < F8_SLOTS; ++i) { mbar_init(&st_full[i], 1); mbar_init(&st_empty[i], 3); }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -137,64 +176,124 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
   auto fail = [&](int code) { if (p.status) atomicCAS(p.status, 0, code); *abort_flag = 1; };
 
   if (warp == 0) {
-    // ---------------- TMA: this CTA's Q atoms once, then its atoms of the gathered KV rows ----------------
+    // ---------------- TMA: this CTA's Q atoms once, then its pieces of the gathered KV rows ----------------
     if (lane == 0 && n_tiles > 0) {
       tma_prefetch_desc(&tm_q); tma_prefetch_desc(&tm_kv);
+      if (F8) { tma_prefetch_desc(&tm_sc); if (rope) tma_prefetch_desc(&tm_pe); }
       mbar_arrive_expect_tx(q_full, nac * Q_ATOM);
       for (int la = 0; la < nac; ++la) tma_load_3d(sQ + la * Q_ATOM, &tm_q, q_full, atom_of(hh, la) * 64, 0, t);
     }
+    // KT == 32: one key per lane; the next tile's slot is loaded while this tile's gathers are issued
+    int next = k_begin + lane < k_end ? __ldg(idx_t + k_begin + lane) : 0;
     for (int j = 0; j < n_tiles; ++j) {
-      const int s = j % STAGES;
-      const int key = k_begin + j * KT + lane;                 // KT == 32: one key per lane
-      int slot = key < k_end ? __ldg(idx_t + key) : 0;
+      int slot = next;
+      const int nk = k_begin + (j + 1) * KT + lane;
+      next = (j + 1 < n_tiles && nk < k_end) ? __ldg(idx_t + nk) : 0;
       if (slot < 0) slot = 0;                                  // masked in softmax; keep the address valid
+      const int s = F8 ? j % F8_SLOTS : j % STAGES;
+      uint64_t* full = F8 ? &st_full[s] : &kv_full[s];
       int ok = 1;
       if (lane == 0) {
-        ok = mbar_wait(&kv_empty[s], ((j / STAGES) & 1) ^ 1) ? 1 : 0;
-        if (ok) mbar_arrive_expect_tx(&kv_full[s], kv_bytes);
+        ok = (F8 ? mbar_wait(&st_empty[s], ((j / F8_SLOTS) & 1) ^ 1)
+                 : mbar_wait(&kv_empty[s], ((j / STAGES) & 1) ^ 1)) ? 1 : 0;
+        if (ok) mbar_arrive_expect_tx(full, F8 ? 8192 + KT * F8_SC_BOX + (rope ? KV_ATOM : 0) : nac * KV_ATOM);
         else fail(kErrTimeoutEmpty);
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok || *abort_flag) break;
-      // lane (la, g): local atom la = lane / 8, row group g = lane % 8 (rows 4g..4g+3)
-      const int la = int(lane >> 3), g = int(lane & 7);
+      // lane (part, g): part = lane / 8, row group g = lane % 8 (rows 4g..4g+3)
+      const int part = int(lane >> 3), g = int(lane & 7);
       const int r0 = __shfl_sync(0xffffffffu, slot, 4 * g), r1 = __shfl_sync(0xffffffffu, slot, 4 * g + 1);
       const int r2 = __shfl_sync(0xffffffffu, slot, 4 * g + 2), r3 = __shfl_sync(0xffffffffu, slot, 4 * g + 3);
-      if (la < 4)
-        tma_gather4(sKV + s * KV_STAGE + la * KV_ATOM + g * 4 * 128, &tm_kv, &kv_full[s], atom_of(hh, la) * 64, r0,
-                    r1, r2, r3);
-      if (nac == 5 && la == 0)                                 // the RoPE atom (CTA 0 of MLA rows)
-        tma_gather4(sKV + s * KV_STAGE + 4 * KV_ATOM + g * 4 * 128, &tm_kv, &kv_full[s], 8 * 64, r0, r1, r2, r3);
+      if constexpr (F8) {
+        uint8_t* sl = sST + s * F8_SLOT;
+        if (part < 2)            // value bytes [256 hh + 128 part, +128) of each row
+          tma_gather4(sl + F8_VAL + part * 4096 + g * 512, &tm_kv, full, hh * 256 + part * 128, r0, r1, r2, r3);
+        else if (part == 2)      // scale bytes [512, 528) of the four rows
+          tma_gather4(sl + F8_SC + g * 128, &tm_sc, full, 512, r0, r1, r2, r3);
+        else if (rope)           // fp16 RoPE key, swizzled into the operand layout
+          tma_gather4(sl + F8_PE + g * 512, &tm_pe, full, 0, r0, r1, r2, r3);
+      } else {
+        if (part < 4)
+          tma_gather4(sKV + s * KV_STAGE + part * KV_ATOM + g * 4 * 128, &tm_kv, full, atom_of(hh, part) * 64, r0, r1,
+                      r2, r3);
+        if (rope && part == 0)                                 // the RoPE atom (CTA 0 of MLA rows)
+          tma_gather4(sKV + s * KV_STAGE + 4 * KV_ATOM + g * 4 * 128, &tm_kv, full, 8 * 64, r0, r1, r2, r3);
+      }
       __syncwarp();
+    }
+  } else if (F8 && (warp == 2 || warp == 3)) {
+    // ---------------- fp8 -> fp16 value atoms (each warp converts 16 of the tile's 32 rows) ----------------
+    const int cw = int(warp) - 2;
+    for (int j = 0; j < n_tiles; ++j) {
+      const int s8 = j % F8_SLOTS, s = j % F8_STAGES;
+      int ok = 1;
+      if (lane == 0) {
+        ok = (mbar_wait(&st_full[s8], (j / F8_SLOTS) & 1) && mbar_wait(&kv_empty[s], ((j / F8_STAGES) & 1) ^ 1)) ? 1
+                                                                                                             : 0;
+        if (!ok) fail(kErrTimeoutFull);
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok || *abort_flag) break;
+      const uint8_t* sl = sST + s8 * F8_SLOT;
+      uint8_t* dst = sKV + s * F8_KV_STAGE;
+#pragma unroll 2
+      for (int i = 0; i < 8; ++i) {
+        // task: row, local atom la, 16-value chunk c; a warp's 32 lanes read four whole 128-byte row pieces
+        const int id = cw * 256 + i * 32 + int(lane);
+        const int row = id >> 4, la = (id >> 2) & 3, c = id & 3;
+        const uint4 v = *reinterpret_cast<const uint4*>(sl + F8_VAL + (la >> 1) * 4096 + row * 128 + (la & 1) * 64 +
+                                                        c * 16);
+        const uint32_t sb = sl[F8_SC + (row >> 2) * 128 + (row & 3) * F8_SC_BOX + hh * 4 + la];
+        const __half hs = __float2half_rn(ue8m0_to_float(sb));
+        const uint32_t s2 = uint32_t(*reinterpret_cast<const uint16_t*>(&hs)) * 0x10001u;
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        uint32_t h[8];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          h[2 * k] = hmul2_u32(e4m3x2_to_f16x2(w[k] & 0xffffu), s2);
+          h[2 * k + 1] = hmul2_u32(e4m3x2_to_f16x2(w[k] >> 16), s2);
+        }
+        uint8_t* rowp = dst + la * KV_ATOM + row * 128;
+        const int sw = row & 7;
+        *reinterpret_cast<uint4*>(rowp + (((2 * c) ^ sw) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
+        *reinterpret_cast<uint4*>(rowp + (((2 * c + 1) ^ sw) << 4)) = make_uint4(h[4], h[5], h[6], h[7]);
+      }
+      fence_proxy_async();                   // generic-proxy stores -> visible to the tensor core's operand reads
+      __syncwarp();
+      if (lane == 0) { mbar_arrive(&kv_full[s]); mbar_arrive(&st_empty[s8]); }
     }
   } else if (warp == 1) {
     // ---------------- MMA ----------------
     if (elect_one() && n_tiles > 0) {
-      const uint32_t id_qk = idesc_bf16(HM, KT);
-      const uint32_t id_pv = idesc_bf16(HM, DHALF) | (1u << 16);   // B (V) MN-major
+      const uint32_t id_qk = F8 ? idesc_f16(HM, KT) : idesc_bf16(HM, KT);
+      const uint32_t id_pv = (F8 ? idesc_f16(HM, DHALF) : idesc_bf16(HM, DHALF)) | (1u << 16);   // B (V) MN-major
       bool ok = mbar_wait(q_full, 0);
       if (!ok) fail(kErrTimeoutFull);
       auto issue_qk = [&](int j) -> bool {
-        const int s = j % STAGES, b = j & 1;
-        if (!mbar_wait(&kv_full[s], (j / STAGES) & 1)) { fail(kErrTimeoutFull); return false; }
+        const int s = j % NST, b = j & 1, s8 = j % F8_SLOTS;
+        if (!mbar_wait(&kv_full[s], (j / NST) & 1)) { fail(kErrTimeoutFull); return false; }
+        if (F8 && rope && !mbar_wait(&st_full[s8], (j / F8_SLOTS) & 1)) { fail(kErrTimeoutFull); return false; }
         tc_fence_after();
         for (int la = 0; la < nac; ++la) {
+          const uint8_t* kb = (F8 && la == 4) ? sST + s8 * F8_SLOT + F8_PE : sKV + s * STAGE_B + la * KV_ATOM;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
             mma_f16_ss(tmem + TM_S + b * TM_S_STRIDE, smem_desc_sw128(sQ + la * Q_ATOM + kk * 32),
-                       smem_desc_sw128(sKV + s * KV_STAGE + la * KV_ATOM + kk * 32), id_qk, (la | kk) > 0);
+                       smem_desc_sw128(kb + kk * 32), id_qk, (la | kk) > 0);
         }
         mma_commit(&s_full[b]);
+        if (F8) mma_commit(&st_empty[s8]);   // the slot's RoPE atom has been read
         return true;
       };
       auto issue_pv = [&](int j) -> bool {
-        const int s = j % STAGES, b = j & 1;
+        const int s = j % NST, b = j & 1;
         if (!mbar_wait(&p_full[b], (j >> 1) & 1)) { fail(kErrTimeoutFull); return false; }
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < KT / 16; ++k)
           mma_f16_ts(tmem + TM_O, tmem + TM_S + b * TM_S_STRIDE + 8 * k,
-                     desc_mn_sw128(sKV + s * KV_STAGE + k * 16 * 128, KV_ATOM, 1024), id_pv,
+                     desc_mn_sw128(sKV + s * STAGE_B + k * 16 * 128, KV_ATOM, 1024), id_pv,
                      (j > 0 || k > 0) ? 1u : 0u);
         mma_commit(&pv_done[b]);
         mma_commit(&kv_empty[s]);
@@ -282,7 +381,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
         const float a0 = exp2f(sv[i] - m_ref), a1 = exp2f(sv[i + 1] - m_ref);
         rs0 += a0;
         rs1 += a1;
-        pk[i / 2] = pack_bf16x2(a0, a1);
+        pk[i / 2] = F8 ? pack_f16x2(a0, a1) : pack_bf16x2(a0, a1);
       }
       tmem_st_32x32b_x16(t_lane + TM_S + b * TM_S_STRIDE, pk);   // P over the first KT/2 columns of S(j)
       // my exchange buffer b is free again: P (issued above) is computed from its values, so their loads are done
@@ -375,6 +474,59 @@ __global__ void mla_combine_kernel(const float* __restrict__ part_o, const float
   }
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// fp8 latent rows.  A cached token row of the fp8 format holds r = 512 e4m3 latent values quantised per 64-dim atom
+// (UE8M0 power-of-two scale, the smallest 2^e with amax / 2^e <= 448), the 8 scale bytes padded to 16, and for MLA
+// the 64 RoPE-key dims as fp16: 656 bytes per MLA token (1152 in bf16), 528 per latent-MQA token (its RoPE dims are
+// the last latent atom).  One warp per row: lane l quantises dims [16 l, 16 l + 16), lanes 4a..4a+3 form atom a.
+// ---------------------------------------------------------------------------------------------------------------
+__global__ void latent_store_fp8_kernel(const __nv_bfloat16* __restrict__ rows, int n, int ld, int D,
+                                        const int* __restrict__ slots, uint8_t* __restrict__ cache, int RB) {
+  cb::pdl_entry();
+  const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (w >= n) return;
+  const int slot = slots[w];
+  if (slot < 0) return;                                   // uniform per warp
+  const __nv_bfloat16* x = rows + size_t(w) * ld;
+  uint8_t* dst = cache + size_t(slot) * RB;
+  const uint4 raw0 = *reinterpret_cast<const uint4*>(x + lane * 16);
+  const uint4 raw1 = *reinterpret_cast<const uint4*>(x + lane * 16 + 8);
+  const uint32_t u[8] = {raw0.x, raw0.y, raw0.z, raw0.w, raw1.x, raw1.y, raw1.z, raw1.w};
+  float v[16];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) { v[2 * i] = bf16_lo(u[i]); v[2 * i + 1] = bf16_hi(u[i]); }
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));
+  amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 2));
+  const uint32_t sb = ue8m0_for_amax(amax);
+  const float inv = ue8m0_inv(sb);
+  uint4 q;
+  q.x = pack_fp8x4(v[0] * inv, v[1] * inv, v[2] * inv, v[3] * inv);
+  q.y = pack_fp8x4(v[4] * inv, v[5] * inv, v[6] * inv, v[7] * inv);
+  q.z = pack_fp8x4(v[8] * inv, v[9] * inv, v[10] * inv, v[11] * inv);
+  q.w = pack_fp8x4(v[12] * inv, v[13] * inv, v[14] * inv, v[15] * inv);
+  reinterpret_cast<uint4*>(dst)[lane] = q;
+  // scale bytes of atoms 0..7 (lanes 0, 4, ..., 28) -> bytes [512, 528), the last 8 zero
+  uint32_t lo = 0, hi = 0;
+#pragma unroll
+  for (int a = 0; a < 8; ++a) {
+    const uint32_t b = __shfl_sync(0xffffffffu, sb, 4 * a);
+    if (a < 4) lo |= b << (8 * a); else hi |= b << (8 * (a - 4));
+  }
+  if (lane == 0) *reinterpret_cast<uint4*>(dst + 512) = make_uint4(lo, hi, 0u, 0u);
+  if (D == 576 && lane < 16) {                            // RoPE key dims 512..575 -> fp16 at bytes [528, 656)
+    const uint2 r2 = *reinterpret_cast<const uint2*>(x + 512 + lane * 4);
+    __half2 h0 = __floats2half2_rn(bf16_lo(r2.x), bf16_hi(r2.x));
+    __half2 h1 = __floats2half2_rn(bf16_lo(r2.y), bf16_hi(r2.y));
+    uint2 o;
+    o.x = *reinterpret_cast<uint32_t*>(&h0);
+    o.y = *reinterpret_cast<uint32_t*>(&h1);
+    reinterpret_cast<uint2*>(dst + 528)[lane] = o;
+  }
+}
+
 static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   if (!fn) {
@@ -389,42 +541,80 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 }  // namespace mla
 
-// q [T,H,D], kv [S,D] bf16 with D = 576 (MLA) or 512 (latent MQA); idx [T,K]; out [T,H,512] bf16.
-// part_o/part_ml: workspace for n_splits > 1
-// (sizes T*n_splits*H*512 and T*n_splits*H*2 floats).
-cudaError_t sparse_mla(const void* q, int T, int H, const void* kv, int S, const int* idx, int K, float scale,
-                       int n_splits, float* part_o, float* part_ml, void* out, int* status, cudaStream_t s,
-                       const float* sink, int D) {
+namespace {
+
+CUresult make_map(CUtensorMap* m, CUtensorMapDataType dt, int rank, const void* base, const cuuint64_t* dims,
+                  const cuuint64_t* strides, const cuuint32_t* box, CUtensorMapSwizzle sw) {
+  const cuuint32_t es[3] = {1, 1, 1};
+  return mla::encode_fn()(m, dt, rank, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+template <int NA, bool F8>
+cudaError_t launch_sparse_mla(const CUtensorMap& tq, const CUtensorMap& tkv, const CUtensorMap& tsc,
+                              const CUtensorMap& tpe, const mla::Params& p, int T, int n_splits, cudaStream_t s) {
+  using namespace mla;
+  cudaError_t e = smem_optin(sparse_mla_kernel<NA, F8>, smem_bytes<F8>());
+  if (e != cudaSuccess) return e;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1; attr[0].val.clusterDim.y = 2; attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;     // see cb::pdl_entry
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(T, 2, n_splits);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = smem_bytes<F8>();
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, sparse_mla_kernel<NA, F8>, tq, tkv, tsc, tpe, p);
+}
+
+// Shared by the bf16 and fp8 entry points: q [T, H, D] (bf16, or fp16 for fp8 rows); kv rows [S, row_bytes].
+cudaError_t sparse_mla_any(bool f8, const void* q, int T, int H, const void* kv, int S, const int* idx, int K,
+                           float scale, int n_splits, float* part_o, float* part_ml, void* out, int* status,
+                           cudaStream_t s, const float* sink, int D) {
   using namespace mla;
   if (T == 0) return cudaSuccess;
-  if (H > HM || n_splits < 1 || (D != 576 && D != 512)) return cudaErrorInvalidValue;
-  auto fn = encode_fn();
-  if (!fn) return cudaErrorInvalidValue;
-  CUtensorMap tq, tkv;
+  if (H > HM || H < 1 || n_splits < 1 || (D != 576 && D != 512)) return cudaErrorInvalidValue;
+  if (!encode_fn()) return cudaErrorInvalidValue;
+  const int RB = f8 ? (D == 576 ? 656 : 528) : D * 2;        // bytes of one cached row
+  CUtensorMap tq, tkv, tsc, tpe;
   {
-    cuuint64_t dims[3] = {cuuint64_t(D), cuuint64_t(H), cuuint64_t(T)};
-    cuuint64_t str[2] = {cuuint64_t(D) * 2, cuuint64_t(H) * D * 2};
-    cuuint32_t box[3] = {64, HM, 1};
-    cuuint32_t es[3] = {1, 1, 1};
-    if (fn(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(q), dims, str, box, es,
-           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    const cuuint64_t dims[3] = {cuuint64_t(D), cuuint64_t(H), cuuint64_t(T)};
+    const cuuint64_t str[2] = {cuuint64_t(D) * 2, cuuint64_t(H) * D * 2};
+    const cuuint32_t box[3] = {64, HM, 1};
+    if (make_map(&tq, f8 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, q, dims, str, box,
+                 CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
       return cudaErrorInvalidValue;
   }
-  {
-    cuuint64_t dims[2] = {cuuint64_t(D), cuuint64_t(S)};
-    cuuint64_t str[1] = {cuuint64_t(D) * 2};
-    cuuint32_t box[2] = {64, 1};
-    cuuint32_t es[2] = {1, 1};
-    if (fn(&tkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(kv), dims, str, box, es,
-           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+  if (!f8) {
+    const cuuint64_t dims[2] = {cuuint64_t(D), cuuint64_t(S)};
+    const cuuint64_t str[1] = {cuuint64_t(RB)};
+    const cuuint32_t box[2] = {64, 1};
+    if (make_map(&tkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, kv, dims, str, box, CU_TENSOR_MAP_SWIZZLE_128B) !=
+        CUDA_SUCCESS)
       return cudaErrorInvalidValue;
-  }
-  {
-    cudaError_t e = D == 576 ? smem_optin(sparse_mla_kernel<9>, smem_bytes<9>())
-                             : smem_optin(sparse_mla_kernel<8>, smem_bytes<8>());
-    if (e != cudaSuccess) return e;
+    tsc = tkv;
+    tpe = tkv;
+  } else {
+    const cuuint64_t dims[2] = {cuuint64_t(RB), cuuint64_t(S)};
+    const cuuint64_t str[1] = {cuuint64_t(RB)};
+    const cuuint32_t box_v[2] = {128, 1}, box_s[2] = {uint32_t(F8_SC_BOX), 1};
+    if (make_map(&tkv, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, kv, dims, str, box_v, CU_TENSOR_MAP_SWIZZLE_NONE) !=
+            CUDA_SUCCESS ||
+        make_map(&tsc, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, kv, dims, str, box_s, CU_TENSOR_MAP_SWIZZLE_NONE) !=
+            CUDA_SUCCESS)
+      return cudaErrorInvalidValue;
+    tpe = tkv;
+    if (D == 576) {                                            // fp16 RoPE key at bytes [528, 656) of each row
+      const cuuint64_t dpe[2] = {64, cuuint64_t(S)};
+      const cuuint32_t box_pe[2] = {64, 1};
+      if (make_map(&tpe, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, static_cast<const uint8_t*>(kv) + 528, dpe, str, box_pe,
+                   CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
+        return cudaErrorInvalidValue;
+    }
   }
   Params p;
   p.idx = idx; p.K = K; p.H = H; p.n_splits = n_splits;
@@ -434,27 +624,45 @@ cudaError_t sparse_mla(const void* q, int T, int H, const void* kv, int S, const
   p.out = reinterpret_cast<__nv_bfloat16*>(out);
   p.status = status;
   p.sink = sink;
-  cudaLaunchAttribute attr[2];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1; attr[0].val.clusterDim.y = 2; attr[0].val.clusterDim.z = 1;
-  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;     // see cb::pdl_entry
-  attr[1].val.programmaticStreamSerializationAllowed = 1;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(T, 2, n_splits);
-  cfg.blockDim = dim3(256);
-  cfg.dynamicSmemBytes = SMEM;
-  cfg.stream = s;
-  cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 2 : 1;
-  {
-    cudaError_t e = D == 576 ? cudaLaunchKernelEx(&cfg, sparse_mla_kernel<9>, tq, tkv, p)
-                             : cudaLaunchKernelEx(&cfg, sparse_mla_kernel<8>, tq, tkv, p);
-    if (e != cudaSuccess) return e;
-  }
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e;
+  if (f8) e = D == 576 ? launch_sparse_mla<9, true>(tq, tkv, tsc, tpe, p, T, n_splits, s)
+                       : launch_sparse_mla<8, true>(tq, tkv, tsc, tpe, p, T, n_splits, s);
+  else e = D == 576 ? launch_sparse_mla<9, false>(tq, tkv, tsc, tpe, p, T, n_splits, s)
+                    : launch_sparse_mla<8, false>(tq, tkv, tsc, tpe, p, T, n_splits, s);
+  if (e != cudaSuccess) return e;
+  e = cudaGetLastError();
   if (e != cudaSuccess || n_splits == 1) return e;
-  cb::launch_k(mla_combine_kernel, dim3(T, H), 128, 0, s, part_o, part_ml, n_splits, H, reinterpret_cast<__nv_bfloat16*>(out),
-                                                sink);
+  cb::launch_k(mla::mla_combine_kernel, dim3(T, H), 128, 0, s, part_o, part_ml, n_splits, H,
+               reinterpret_cast<__nv_bfloat16*>(out), sink);
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+// q [T,H,D], kv [S,D] bf16 with D = 576 (MLA) or 512 (latent MQA); idx [T,K]; out [T,H,512] bf16.
+// part_o/part_ml: workspace for n_splits > 1
+// (sizes T*n_splits*H*512 and T*n_splits*H*2 floats).
+cudaError_t sparse_mla(const void* q, int T, int H, const void* kv, int S, const int* idx, int K, float scale,
+                       int n_splits, float* part_o, float* part_ml, void* out, int* status, cudaStream_t s,
+                       const float* sink, int D) {
+  return sparse_mla_any(false, q, T, H, kv, S, idx, K, scale, n_splits, part_o, part_ml, out, status, s, sink, D);
+}
+
+// The same attention over fp8 cache rows (656 bytes per MLA row, 528 per latent-MQA row; see latent_store_fp8),
+// with q [T,H,D] in fp16.
+cudaError_t sparse_mla_fp8(const void* q, int T, int H, const void* kv, int S, const int* idx, int K, float scale,
+                           int n_splits, float* part_o, float* part_ml, void* out, int* status, cudaStream_t s,
+                           const float* sink, int D) {
+  return sparse_mla_any(true, q, T, H, kv, S, idx, K, scale, n_splits, part_o, part_ml, out, status, s, sink, D);
+}
+
+// rows [n, D] bf16 (row stride ld elements, D = 576 or 512) -> fp8 cache rows at slots[i] (slots < 0 skipped).
+cudaError_t latent_store_fp8(const void* rows, int n, int ld, int D, const int* slots, void* cache, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  if ((D != 576 && D != 512) || ld < D || (ld % 8) != 0) return cudaErrorInvalidValue;
+  const int RB = D == 576 ? 656 : 528;
+  cb::launch_k(mla::latent_store_fp8_kernel, dim3((n + 7) / 8), 256, 0, s,
+               reinterpret_cast<const __nv_bfloat16*>(rows), n, ld, D, slots, reinterpret_cast<uint8_t*>(cache), RB);
   return cudaGetLastError();
 }
 

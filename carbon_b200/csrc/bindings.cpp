@@ -322,14 +322,20 @@ void topk_mask(torch::Tensor logits, int64_t Tq, int64_t k, torch::Tensor mask, 
 
 // q [T, H, D], kv [S, D] bf16 (D = 576 MLA latent + RoPE key, or 512 latent MQA), idx [T, K] int32
 // -> out [T, H, 512] bf16
+// Absorbed sparse attention over cached latent rows.  kv bf16 [S, D] with q bf16, or kv uint8 [S, 656 | 528] (the
+// fp8 cache format) with q fp16.
 void sparse_mla(torch::Tensor q, torch::Tensor kv, torch::Tensor idx, double scale, int64_t n_splits,
                 c10::optional<torch::Tensor> work, torch::Tensor out, c10::optional<torch::Tensor> sink) {
   if (sink.has_value() && sink->defined()) {
     CHECK_DT((*sink), at::kFloat); CHECK_CONTIG((*sink)); TORCH_CHECK(sink->numel() >= q.size(1));
   }
-  CHECK_CUDA(q); CHECK_DT(q, at::kBFloat16); CHECK_DT(kv, at::kBFloat16); CHECK_DT(idx, at::kInt);
+  const bool f8 = kv.scalar_type() == at::kByte;
+  CHECK_CUDA(q); CHECK_DT(idx, at::kInt); CHECK_DT(out, at::kBFloat16);
+  if (f8) { CHECK_DT(q, at::kHalf); } else { CHECK_DT(q, at::kBFloat16); CHECK_DT(kv, at::kBFloat16); }
   CHECK_CONTIG(q); CHECK_CONTIG(kv); CHECK_CONTIG(idx); CHECK_CONTIG(out);
-  TORCH_CHECK((q.size(2) == 576 || q.size(2) == 512) && kv.size(1) == q.size(2) && out.size(2) == 512);
+  const int D = q.size(2);
+  TORCH_CHECK((D == 576 || D == 512) && out.size(2) == 512, "sparse_mla: q width 576 or 512, out width 512");
+  TORCH_CHECK(kv.size(1) == (f8 ? (D == 576 ? 656 : 528) : D), "sparse_mla: cache row width");
   const int T = q.size(0), H = q.size(1);
   float* po = nullptr;
   float* pml = nullptr;
@@ -339,9 +345,22 @@ void sparse_mla(torch::Tensor q, torch::Tensor kv, torch::Tensor idx, double sca
     pml = po + int64_t(T) * n_splits * H * 512;
   }
   c10::cuda::CUDAGuard g(q.device());
-  CK(cb::sparse_mla(q.data_ptr(), T, H, kv.data_ptr(), kv.size(0), idx.data_ptr<int>(), idx.size(1), float(scale),
-                    n_splits, po, pml, out.data_ptr(), nullptr, cur_stream(), ptr_or_null<const float>(sink),
-                    int(q.size(2))));
+  auto fn = f8 ? cb::sparse_mla_fp8 : cb::sparse_mla;
+  CK(fn(q.data_ptr(), T, H, kv.data_ptr(), kv.size(0), idx.data_ptr<int>(), idx.size(1), float(scale), n_splits, po,
+        pml, out.data_ptr(), nullptr, cur_stream(), ptr_or_null<const float>(sink), D));
+}
+
+// bf16 latent rows [n, D] (row stride free, unit column stride) -> fp8 cache rows [S, 656 | 528] at slots [n]
+void latent_store_fp8(torch::Tensor rows, torch::Tensor slots, torch::Tensor cache) {
+  CHECK_CUDA(rows); CHECK_DT(rows, at::kBFloat16); CHECK_DT(slots, at::kInt); CHECK_CONTIG(slots);
+  CHECK_DT(cache, at::kByte); CHECK_CONTIG(cache);
+  TORCH_CHECK(rows.dim() == 2 && rows.stride(1) == 1, "latent_store_fp8: rows [n, D] with unit column stride");
+  const int D = rows.size(1);
+  TORCH_CHECK((D == 576 || D == 512) && cache.size(1) == (D == 576 ? 656 : 528), "latent_store_fp8: widths");
+  TORCH_CHECK(slots.numel() == rows.size(0), "latent_store_fp8: one slot per row");
+  c10::cuda::CUDAGuard g(rows.device());
+  CK(cb::latent_store_fp8(rows.data_ptr(), rows.size(0), rows.stride(0), D, slots.data_ptr<int>(), cache.data_ptr(),
+                          cur_stream()));
 }
 
 // Engram row gather: ids [T, C] int32 global rows; data_ptrs / sf_ptrs uint64 [world] (fp8 rows [R_r, dim], UE8M0
@@ -449,6 +468,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("indexer_logits_fp8", &indexer_logits_fp8);
   m.def("topk_mask", &topk_mask);
   m.def("sparse_mla", &sparse_mla);
+  m.def("latent_store_fp8", &latent_store_fp8);
   m.def("engram_gather", &engram_gather);
   m.def("engram_gate", &engram_gate);
   m.def("indexer_topk", &indexer_topk);

@@ -399,6 +399,11 @@ CB_HOST_DEVICE uint32_t idesc_bf16(int M, int N) {
          | (1u << 7) | (1u << 10)    // A, B = bf16
          | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
 }
+// Instruction descriptor, kind::f16 with fp16 A/B, fp32 D, both K-major.
+CB_HOST_DEVICE uint32_t idesc_f16(int M, int N) {
+  return (1u << 4)                   // D format f32 (A, B format 0 = fp16)
+         | (uint32_t(N >> 3) << 17) | (uint32_t(M >> 4) << 24);
+}
 // Instruction descriptor, kind::mxf8f6f4 block-scaled, e4m3 A/B, UE8M0 scales, both K-major.
 CB_HOST_DEVICE uint32_t idesc_mxf8(int M, int N, uint32_t sfa_id, uint32_t sfb_id) {
   return (sfb_id << 4)               // B scale-factor byte id

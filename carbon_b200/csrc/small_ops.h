@@ -95,6 +95,12 @@ cudaError_t topk_slots(const float* logits, int ldo, const int* key_slots, int s
 cudaError_t sparse_mla(const void* q, int T, int H, const void* kv, int S, const int* idx, int K, float scale,
                        int n_splits, float* part_o, float* part_ml, void* out, int* status, cudaStream_t s,
                        const float* sink = nullptr, int D = 576);
+// fp8 cache rows (656 bytes per MLA row, 528 per latent-MQA row), q [T, H, D] fp16
+cudaError_t sparse_mla_fp8(const void* q, int T, int H, const void* kv, int S, const int* idx, int K, float scale,
+                           int n_splits, float* part_o, float* part_ml, void* out, int* status, cudaStream_t s,
+                           const float* sink, int D);
+// bf16 latent rows [n, D] (row stride ld) -> fp8 cache rows at slots (D = 576 or 512)
+cudaError_t latent_store_fp8(const void* rows, int n, int ld, int D, const int* slots, void* cache, cudaStream_t s);
 
 // Engram (engram.cu): fp8 row gather (UE8M0 per 32; table split over ranks by row ranges `bounds`, peer pointers)
 // and the fused per-stream gate + residual update + new sum of squares

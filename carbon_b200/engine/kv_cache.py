@@ -16,6 +16,8 @@ from typing import List, Optional
 import torch
 
 from ..config import ModelConfig
+from ..ops._ext import ext
+from ..ref import ops as R
 from .allocator import BlockAllocator
 
 
@@ -25,8 +27,11 @@ class PagedLatentCache:
         self.page_size = page_size
         self.num_pages = num_pages
         self.num_slots = num_pages * page_size
-        width = cfg.latent_dim
-        self.latent: List[torch.Tensor] = [torch.zeros(self.num_slots, width, dtype=dtype, device=device)
+        # fp8 rows (cfg.kv_fp8): uint8 [slots, row_bytes] in the format of ref.ops.quant_latent_fp8
+        self.fp8 = cfg.kv_fp8
+        width = self.row_bytes(cfg) if self.fp8 else cfg.latent_dim
+        self.latent: List[torch.Tensor] = [torch.zeros(self.num_slots, width, device=device,
+                                                       dtype=torch.uint8 if self.fp8 else dtype)
                                            for _ in range(n_layers)]
         # indexer keys only for layers that run the indexer (index-source layers share their selection)
         self.index_k: List[Optional[torch.Tensor]] = []
@@ -40,8 +45,20 @@ class PagedLatentCache:
     def write_tokens(self, loc: torch.Tensor, ids: torch.Tensor) -> None:
         self.tok.index_copy_(0, loc.long(), ids.to(torch.int32))
 
+    @staticmethod
+    def row_bytes(cfg: ModelConfig) -> int:
+        """Bytes of one cached fp8 latent row (656 for the 512 + 64 MLA row, 528 for a 512-dim latent-MQA row)."""
+        return R.latent_fp8_row_bytes(cfg.kv_lora_rank, cfg.qk_rope_head_dim, cfg.attn_kind == "mla")
+
     def write_latent(self, layer: int, loc: torch.Tensor, rows: torch.Tensor) -> None:
-        self.latent[layer].index_copy_(0, loc.long(), rows.to(self.latent[layer].dtype))
+        if not self.fp8:
+            self.latent[layer].index_copy_(0, loc.long(), rows.to(self.latent[layer].dtype))
+        elif rows.is_cuda:
+            ext().latent_store_fp8(rows.to(torch.bfloat16), loc.to(torch.int32).contiguous(), self.latent[layer])
+        else:
+            cfg = self.cfg
+            q = R.quant_latent_fp8(rows, cfg.kv_lora_rank, cfg.qk_rope_head_dim, cfg.attn_kind == "mla")
+            self.latent[layer].index_copy_(0, loc.long(), q)
 
     def write_index_k(self, layer: int, loc: torch.Tensor, rows: torch.Tensor) -> None:
         self.index_k[layer].index_copy_(0, loc.long(), rows.to(self.index_k[layer].dtype))
@@ -52,4 +69,5 @@ class PagedLatentCache:
     @staticmethod
     def bytes_per_token(cfg: ModelConfig, n_layers: int, elem: int = 2) -> int:
         n_idx = sum(1 for l in range(n_layers) if cfg.has_indexer(l))
-        return cfg.latent_dim * elem * n_layers + cfg.index_head_dim * elem * n_idx
+        lat = PagedLatentCache.row_bytes(cfg) if cfg.kv_fp8 else cfg.latent_dim * elem
+        return lat * n_layers + cfg.index_head_dim * elem * n_idx

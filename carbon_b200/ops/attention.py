@@ -174,26 +174,30 @@ def mla_splits(T: int, K: int, device) -> int:
 
 def sparse_mla(q: torch.Tensor, kv: torch.Tensor, idx: torch.Tensor, scale: float, d_latent: int,
                sink: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Absorbed MQA over latent rows: q [T,H,D], kv [S,D], idx [T,K] int32 (-1 pad) -> o_lat [T,H,d_latent].
-    sink [H]: per-head attention-sink logit (an extra softmax denominator term)."""
+    """Absorbed MQA over latent rows: q [T,H,D], kv [S,D] (or the fp8 cache rows, uint8 [S, row_bytes]), idx [T,K]
+    int32 (-1 pad) -> o_lat [T,H,d_latent].  sink [H]: per-head attention-sink logit (an extra softmax denominator
+    term).  fp8 rows run the kernel's fp16 path (q is rounded to fp16)."""
     T, H, D = q.shape
+    f8 = kv.dtype == torch.uint8
     if q.is_cuda:
         e = ext()
-        if hasattr(e, "sparse_mla") and D in (576, 512) and d_latent == 512 and H <= 128:
+        if D in (576, 512) and d_latent == 512 and H <= 128:
             out = torch.empty(T, H, d_latent, dtype=torch.bfloat16, device=q.device)
             splits = mla_splits(T, idx.shape[1], q.device)
             work = torch.empty(T * splits * H * 514, dtype=torch.float32, device=q.device) if splits > 1 else None
-            e.sparse_mla(q, kv, idx, float(scale), splits, work, out,
+            qk = q.to(torch.float16 if f8 else torch.bfloat16).contiguous()
+            e.sparse_mla(qk, kv, idx, float(scale), splits, work, out,
                          sink.float().contiguous() if sink is not None else None)
             return out
         raise RuntimeError("sparse_mla: the tcgen05 kernel needs D=576 (512 latent + 64 RoPE key) or D=512 (latent "
                            "MQA), d_latent=512, H<=128")
+    mla = D > d_latent
     out = torch.zeros(T, H, d_latent)
     for t in range(T):
         sel = idx[t][idx[t] >= 0].long()
         if sel.numel() == 0:
             continue
-        keys = kv[sel].float()
+        keys = R.dequant_latent_fp8(kv[sel], d_latent, D - d_latent if mla else 0, mla) if f8 else kv[sel].float()
         s = (q[t].float() @ keys.t()) * scale
         if sink is not None:
             s = torch.cat([s, sink.float()[:, None]], dim=-1)

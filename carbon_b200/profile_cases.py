@@ -1,6 +1,6 @@
 """Small, self-contained kernel cases for profiler captures (one launch of one kernel each, a few GB at most).
 
-    python -m carbon_b200.profile_cases gemm|grouped|moe_decode|attn|decode|indexer|indexer_decode|ep_moe|oproj_a2a
+    python -m carbon_b200.profile_cases gemm|grouped|moe_decode|attn|decode|decode_fp8|indexer|indexer_decode|ep_moe|oproj_a2a
 
 Each case sets up inputs larger than L2 where it can, runs its kernel twice (warm-up + the launch to capture) and
 exits 0, so that ``ncu -k regex:<kernel> -s 1 -c 1`` captures exactly one warm launch.
@@ -72,6 +72,21 @@ def decode():
     T, K, S = 32, 2048, 32 * 4096
     q = torch.randn(T, 128, 576, device="cuda").to(torch.bfloat16)
     kv = torch.randn(S, 576, device="cuda").to(torch.bfloat16)
+    idx = torch.stack([torch.randperm(4096, device="cuda")[:K] + b * 4096 for b in range(T)]).int()
+    for _ in range(2):
+        sparse_mla(q, kv, idx, 192 ** -0.5, 512)
+
+
+def decode_fp8():
+    """The decode case over the fp8 cache format (656-byte rows; q in fp16)."""
+    from .ops._ext import ext
+    from .ops.attention import sparse_mla
+
+    T, K, S = 32, 2048, 32 * 4096
+    q = torch.randn(T, 128, 576, device="cuda").to(torch.float16)
+    rows = torch.randn(S, 576, device="cuda").to(torch.bfloat16)
+    kv = torch.empty(S, 656, dtype=torch.uint8, device="cuda")
+    ext().latent_store_fp8(rows, torch.arange(S, dtype=torch.int32, device="cuda"), kv)
     idx = torch.stack([torch.randperm(4096, device="cuda")[:K] + b * 4096 for b in range(T)]).int()
     for _ in range(2):
         sparse_mla(q, kv, idx, 192 ** -0.5, 512)
@@ -153,6 +168,7 @@ def oproj_a2a():
 
 if __name__ == "__main__":
     {"gemm": gemm, "grouped": grouped, "moe_decode": moe_decode, "attn": attn, "decode": decode,
+     "decode_fp8": decode_fp8,
      "indexer": indexer, "indexer_decode": indexer_decode, "ep_moe": ep_moe, "oproj_a2a": oproj_a2a}[sys.argv[1]]()
     torch.cuda.synchronize()
     print("ok", sys.argv[1])

@@ -202,6 +202,53 @@ def dequant_fp8_rows32(q: torch.Tensor, sf: torch.Tensor) -> torch.Tensor:
     return q.float() * torch.pow(2.0, sf.float() - 127.0).repeat_interleave(32, dim=1)
 
 
+# ----------------------------------------------------------------------------------------------------------------------
+# fp8 latent KV rows (the paged cache's quantised format)
+# ----------------------------------------------------------------------------------------------------------------------
+LATENT_ATOM = 64
+
+
+def latent_fp8_row_bytes(r: int, dr: int, mla: bool) -> int:
+    """Bytes of one cached token row in the fp8 format: r e4m3 latent values (one UE8M0 scale per 64-dim atom),
+    the scale bytes padded to 16, then (MLA) the dr RoPE-key dims as fp16.  r = 512, dr = 64: 656 bytes for MLA
+    (1152 in bf16), 528 for latent MQA (1024 in bf16; its RoPE dims are the last atom of the latent)."""
+    na = r // LATENT_ATOM
+    return r + (na + 15) // 16 * 16 + (2 * dr if mla else 0)
+
+
+def quant_latent_fp8(rows: torch.Tensor, r: int, dr: int, mla: bool) -> torch.Tensor:
+    """[n, r (+ dr)] latent rows -> [n, row_bytes] uint8 in the fp8 cache format.  Each 64-dim atom gets the
+    smallest power-of-two scale 2^e with amax / 2^e <= 448 (e clamped to [-126, 127]; 2^0 for an all-zero atom)
+    and its values are rounded to nearest-even e4m3."""
+    n = rows.shape[0]
+    na = r // LATENT_ATOM
+    rb = latent_fp8_row_bytes(r, dr, mla)
+    x = rows[:, :r].float().reshape(n, na, LATENT_ATOM)
+    amax = x.abs().amax(-1)
+    m, ex = torch.frexp(amax / FP8_MAX)
+    e = torch.where(amax > 0, ex - (m == 0.5).to(ex.dtype), torch.zeros_like(ex)).clamp(-126, 127)
+    q = (x / torch.pow(2.0, e.float())[..., None]).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
+    out = torch.zeros(n, rb, dtype=torch.uint8, device=rows.device)
+    out[:, :r] = q.reshape(n, r).view(torch.uint8)
+    out[:, r:r + na] = (e + 127).to(torch.uint8)
+    if mla:
+        out[:, rb - 2 * dr:] = rows[:, r:r + dr].to(torch.float16).contiguous().view(torch.uint8)
+    return out
+
+
+def dequant_latent_fp8(rows8: torch.Tensor, r: int, dr: int, mla: bool) -> torch.Tensor:
+    """Inverse of ``quant_latent_fp8``: [n, row_bytes] uint8 -> [n, r (+ dr)] float32."""
+    n = rows8.shape[0]
+    na = r // LATENT_ATOM
+    rb = latent_fp8_row_bytes(r, dr, mla)
+    q = rows8[:, :r].contiguous().view(torch.float8_e4m3fn).float().reshape(n, na, LATENT_ATOM)
+    s = torch.pow(2.0, rows8[:, r:r + na].float() - 127.0)
+    x = (q * s[..., None]).reshape(n, r)
+    if mla:
+        x = torch.cat([x, rows8[:, rb - 2 * dr:].contiguous().view(torch.float16).float()], dim=1)
+    return x
+
+
 def fake_quant_mxfp4(x: torch.Tensor, block: int = 32) -> torch.Tensor:
     """Round x (any shape, last dim a multiple of 32) to MXFP4 values in its own dtype: per 32-element block the
     scale of ``quant_mxfp4`` and the nearest e2m1 value, ties to the smaller magnitude (identical to

@@ -81,10 +81,11 @@ def test_small_model_vs_oracle(plen):
 
 
 @pytest.mark.parametrize("plen", [60, 280])
-def test_decode_matches_prefill_of_longer_prompt(plen):
+@pytest.mark.parametrize("kv_fp8", [False, True])
+def test_decode_matches_prefill_of_longer_prompt(plen, kv_fp8):
     """logits of decode(token n) after prefill(n) == logits of prefill(n+1) (absorbed vs non-absorbed MLA,
-    latent cache vs in-batch keys, indexer top-k in both)."""
-    cfg = _cfg()
+    latent cache vs in-batch keys, indexer top-k in both); kv_fp8: decode reads the fp8 cache rows."""
+    cfg = _cfg().replace(kv_fp8=kv_fp8)
     src = WeightSource(cfg, seed=7)
     eng = Engine(cfg, device="cuda", source=src, num_pages=32, page_size=64)
     g = torch.Generator().manual_seed(3)
@@ -98,8 +99,9 @@ def test_decode_matches_prefill_of_longer_prompt(plen):
     assert torch.corrcoef(torch.stack([dec, full]))[0, 1] > 0.99
 
 
-def test_cuda_graph_decode_matches_eager():
-    cfg = small_gpu_config().replace(n_layers=2)
+@pytest.mark.parametrize("kv_fp8", [False, True])
+def test_cuda_graph_decode_matches_eager(kv_fp8):
+    cfg = small_gpu_config().replace(n_layers=2, kv_fp8=kv_fp8)
     src = WeightSource(cfg, seed=3)
     g = torch.Generator().manual_seed(2)
     prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (70, 33, 5)]
@@ -147,8 +149,9 @@ def test_v4_latent_mqa_model_vs_oracle(plen):
     assert torch.corrcoef(torch.stack([got, exp]))[0, 1] > 0.98
 
 
-def test_v4_latent_mqa_decode_matches_prefill():
-    cfg = _v4_cfg()
+@pytest.mark.parametrize("kv_fp8", [False, True])
+def test_v4_latent_mqa_decode_matches_prefill(kv_fp8):
+    cfg = _v4_cfg().replace(kv_fp8=kv_fp8)
     src = WeightSource(cfg, seed=7)
     eng = Engine(cfg, device="cuda", source=src, num_pages=32, page_size=64)
     g = torch.Generator().manual_seed(3)
