@@ -166,6 +166,32 @@ void mhc_post_mix(torch::Tensor X, torch::Tensor out, torch::Tensor post, torch:
                       X.size(2), Xn.data_ptr(), sumsq.data_ptr<float>(), cur_stream()));
 }
 
+// Fused decode-size mHC boundary: X [T, 4, D] bf16 in place; out (optional) the previous sublayer's output [T, D]
+// with its post [T, 4] / comb [T, 16]; fn [48, 4D] bf16 (hi; lo), base [24], scale [3] and norm weight w [D] of the
+// next sublayer -> y [T, D] bf16, q [T, D] fp8 + sf (SF tiles), and that sublayer's pre / post / comb
+void mhc_boundary_small(torch::Tensor X, c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> post_in,
+                        c10::optional<torch::Tensor> comb_in, torch::Tensor fn, torch::Tensor base, torch::Tensor scale,
+                        int64_t iters, double hc_eps, double rms_eps, torch::Tensor w, torch::Tensor y,
+                        c10::optional<torch::Tensor> q, c10::optional<torch::Tensor> sf, torch::Tensor pre_out,
+                        torch::Tensor post_out, torch::Tensor comb_out) {
+  CHECK_CUDA(X); CHECK_DT(X, at::kBFloat16); CHECK_CONTIG(X); CHECK_DT(fn, at::kBFloat16); CHECK_CONTIG(fn);
+  CHECK_DT(w, at::kFloat); CHECK_DT(y, at::kBFloat16); CHECK_CONTIG(y);
+  TORCH_CHECK(X.dim() == 3 && X.size(1) == 4, "mhc_boundary_small: X [T, 4, D]");
+  const int T = X.size(0), D = X.size(2);
+  TORCH_CHECK(fn.size(0) == 48 && fn.size(1) == 4 * D, "mhc_boundary_small: fn [48, 4D]");
+  if (out.has_value()) {
+    CHECK_DT((*out), at::kBFloat16); CHECK_CONTIG((*out));
+    TORCH_CHECK(post_in.has_value() && comb_in.has_value(), "mhc_boundary_small: post / comb of the output");
+  }
+  c10::cuda::CUDAGuard g(X.device());
+  CK(cb::mhc_boundary_small(X.data_ptr(), T, D, ptr_or_null<const void>(out), ptr_or_null<const float>(post_in),
+                            ptr_or_null<const float>(comb_in), fn.data_ptr(), base.data_ptr<float>(),
+                            scale.data_ptr<float>(), int(iters), float(hc_eps), float(rms_eps), w.data_ptr<float>(),
+                            y.data_ptr(), ptr_or_null<void>(q), ptr_or_null<uint32_t>(sf), pre_out.data_ptr<float>(),
+                            post_out.data_ptr<float>(), comb_out.data_ptr<float>(), cur_stream()));
+  if (q.has_value()) CK(cb::sf_pad(reinterpret_cast<uint32_t*>(sf->data_ptr()), T, D, cur_stream()));
+}
+
 void embed_hc(torch::Tensor table, int64_t row_lo, torch::Tensor ids, torch::Tensor X,
               c10::optional<torch::Tensor> sumsq) {
   CHECK_CUDA(table); CHECK_DT(table, at::kBFloat16); CHECK_CONTIG(table); CHECK_DT(ids, at::kInt);
@@ -455,6 +481,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mhc_coeffs", &mhc_coeffs);
   m.def("mhc_head_coeffs", &mhc_head_coeffs);
   m.def("mhc_pre_norm", &mhc_pre_norm);
+  m.def("mhc_boundary_small", &mhc_boundary_small);
   m.def("mhc_post_mix", &mhc_post_mix);
   m.def("embed_hc", &embed_hc);
   m.def("row_sumsq", &row_sumsq);

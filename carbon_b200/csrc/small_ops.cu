@@ -8,6 +8,7 @@
 // instruction sequence.
 #include "common.cuh"
 #include "small_ops.h"
+#include "ptx.cuh"
 
 namespace cb {
 
@@ -811,6 +812,290 @@ cudaError_t mhc_post_mix(const void* X, const void* out, const float* post, cons
   cb::launch_k(mhc_post_mix_kernel, T, 256, 0, s, reinterpret_cast<const __nv_bfloat16*>(X),
                                         reinterpret_cast<const __nv_bfloat16*>(out), post, comb, D,
                                         reinterpret_cast<__nv_bfloat16*>(Xn), sumsq);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Fused mHC boundary for decode-sized batches: one launch per boundary instead of post-mix, statistics GEMM,
+// coefficients and pre-norm (four launches, each re-reading the residual streams).  A cluster of 8 CTAs serves TT
+// tokens; CTA c owns columns [c D/8, (c+1) D/8) of every stream (128 threads, 8 columns each).
+//   A  post-mix (when the previous sublayer's output is given): X_o = bf16(post_o out + Σ_i comb[i][o] X_i), written
+//      in place; Σx² of the new streams (or of X as it is, for the first boundary of a step)
+//   B  the next sublayer's 48 statistics (fn rows: 24 hi + 24 lo parts) over this CTA's columns of the 4 streams,
+//      partial sums exchanged through distributed shared memory (every CTA sums all 8 partials itself)
+//   C  coefficients: pre / post through sigmoids, comb through Sinkhorn (16 lanes, one matrix entry each)
+//   D  pre-mix a = bf16(Σ_s pre_s X_s), RMSNorm with the cluster-wide Σa², bf16 output and fp8 1x128 quantisation
+// The arithmetic of each step is that of the separate kernels (mhc_post_mix, mhc_coeffs, mhc_pre_norm); only the
+// summation order of the reductions differs.  Reference role: the Mega-mHC boundary kernel of the reference
+// (king_v10/bundle_v9/cuda_moe_prefill.py:862 sm100_mega_mhc; decode use in dec/prenorm_pair.py).
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int kBndCluster = 8, kBndThreads = 128, kBndStats = 48;
+
+template <int TT>
+__global__ void __cluster_dims__(kBndCluster, 1, 1) __launch_bounds__(kBndThreads)
+    mhc_boundary_small_kernel(__nv_bfloat16* X, int T, int D, const __nv_bfloat16* __restrict__ out,
+                              const float* __restrict__ post_in, const float* __restrict__ comb_in,
+                              const __nv_bfloat16* __restrict__ fn, const float* __restrict__ base,
+                              const float* __restrict__ scale, int iters, float hc_eps, float rms_eps,
+                              const float* __restrict__ w, __nv_bfloat16* __restrict__ y, uint8_t* __restrict__ q,
+                              uint32_t* __restrict__ sf, int row_blocks, float* __restrict__ pre_out,
+                              float* __restrict__ post_out, float* __restrict__ comb_out) {
+  cb::pdl_entry();
+  __shared__ float part[kBndThreads / 32][TT * 8];           // per-warp partials of one 8-row group
+  __shared__ float red[TT][kBndStats + 1];                    // this CTA's stats partials + Σx² (read cluster-wide)
+  __shared__ float tot[TT][kBndStats + 1];
+  __shared__ float coef[TT][24];                              // pre[4], post[4], comb[16]
+  __shared__ float red2[TT];
+  __shared__ float nrm[TT];
+  const int c = int(cluster_ctarank());
+  const int Dc = D / kBndCluster;
+  const int k = threadIdx.x, lane = k & 31, wid = k >> 5;
+  const bool act = k * 8 < Dc;
+  const int col = c * Dc + k * 8;
+  const size_t FD = size_t(4) * D;
+  float xn[TT][4][8];
+  float ss[TT];
+  // ---- A: post-mix (or plain read) ----
+#pragma unroll
+  for (int i = 0; i < TT; ++i) {
+    const int t = blockIdx.y * TT + i;
+    ss[i] = 0.f;
+#pragma unroll
+    for (int s = 0; s < 4; ++s)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) xn[i][s][j] = 0.f;
+    if (!act || t >= T) continue;
+    __nv_bfloat16* xr = X + size_t(t) * FD;
+    float xs[4][8];
+#pragma unroll
+    for (int s = 0; s < 4; ++s) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(xr + size_t(s) * D + col);
+      xs[s][0] = bf16_lo(raw.x); xs[s][1] = bf16_hi(raw.x); xs[s][2] = bf16_lo(raw.y); xs[s][3] = bf16_hi(raw.y);
+      xs[s][4] = bf16_lo(raw.z); xs[s][5] = bf16_hi(raw.z); xs[s][6] = bf16_lo(raw.w); xs[s][7] = bf16_hi(raw.w);
+    }
+    if (out) {
+      float ov[8];
+      const uint4 r0 = *reinterpret_cast<const uint4*>(out + size_t(t) * D + col);
+      ov[0] = bf16_lo(r0.x); ov[1] = bf16_hi(r0.x); ov[2] = bf16_lo(r0.y); ov[3] = bf16_hi(r0.y);
+      ov[4] = bf16_lo(r0.z); ov[5] = bf16_hi(r0.z); ov[6] = bf16_lo(r0.w); ov[7] = bf16_hi(r0.w);
+      float pst[4], cbm[16];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) pst[j] = post_in[t * 4 + j];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) cbm[j] = comb_in[t * 16 + j];
+#pragma unroll
+      for (int o = 0; o < 4; ++o) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float a = pst[o] * ov[j];
+#pragma unroll
+          for (int ii = 0; ii < 4; ++ii) a += cbm[ii * 4 + o] * xs[ii][j];
+          xn[i][o][j] = __bfloat162float(__float2bfloat16_rn(a));
+        }
+      }
+#pragma unroll
+      for (int o = 0; o < 4; ++o) {
+        uint4 wv;
+        wv.x = pack_bf16x2(xn[i][o][0], xn[i][o][1]); wv.y = pack_bf16x2(xn[i][o][2], xn[i][o][3]);
+        wv.z = pack_bf16x2(xn[i][o][4], xn[i][o][5]); wv.w = pack_bf16x2(xn[i][o][6], xn[i][o][7]);
+        *reinterpret_cast<uint4*>(xr + size_t(o) * D + col) = wv;
+      }
+    } else {
+#pragma unroll
+      for (int s = 0; s < 4; ++s)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) xn[i][s][j] = xs[s][j];
+    }
+#pragma unroll
+    for (int s = 0; s < 4; ++s)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss[i] += xn[i][s][j] * xn[i][s][j];
+  }
+  // ---- B: statistics partials over this CTA's columns, 8 fn rows at a time ----
+  for (int r0 = 0; r0 < kBndStats; r0 += 8) {
+    float acc[TT][8];
+#pragma unroll
+    for (int i = 0; i < TT; ++i)
+#pragma unroll
+      for (int rr = 0; rr < 8; ++rr) acc[i][rr] = 0.f;
+    if (act) {
+#pragma unroll
+      for (int rr = 0; rr < 8; ++rr) {
+        const __nv_bfloat16* fr = fn + size_t(r0 + rr) * FD + col;
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+          const uint4 fv = __ldg(reinterpret_cast<const uint4*>(fr + size_t(s) * D));
+          const float f[8] = {bf16_lo(fv.x), bf16_hi(fv.x), bf16_lo(fv.y), bf16_hi(fv.y),
+                              bf16_lo(fv.z), bf16_hi(fv.z), bf16_lo(fv.w), bf16_hi(fv.w)};
+#pragma unroll
+          for (int i = 0; i < TT; ++i)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[i][rr] += xn[i][s][j] * f[j];
+        }
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < TT; ++i)
+#pragma unroll
+      for (int rr = 0; rr < 8; ++rr) {
+        const float v = warp_sum(acc[i][rr]);
+        if (lane == 0) part[wid][i * 8 + rr] = v;
+      }
+    __syncthreads();
+    if (k < TT * 8) {
+      float v = 0.f;
+#pragma unroll
+      for (int ww = 0; ww < kBndThreads / 32; ++ww) v += part[ww][k];
+      red[k / 8][r0 + k % 8] = v;
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < TT; ++i) {
+    const float v = warp_sum(ss[i]);
+    if (lane == 0) part[wid][i] = v;
+  }
+  __syncthreads();
+  if (k < TT) {
+    float v = 0.f;
+#pragma unroll
+    for (int ww = 0; ww < kBndThreads / 32; ++ww) v += part[ww][k];
+    red[k][kBndStats] = v;
+  }
+  cluster_sync();                                            // every CTA's partials are visible cluster-wide
+  for (int e = k; e < TT * (kBndStats + 1); e += kBndThreads) {
+    const uint32_t a = smem_u32(&red[0][0] + e);
+    float v = 0.f;
+    for (int cc = 0; cc < kBndCluster; ++cc) {
+      float x;
+      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x) : "r"(mapa_shared(a, uint32_t(cc))));
+      v += x;
+    }
+    (&tot[0][0])[e] = v;
+  }
+  __syncthreads();
+  // ---- C: coefficients (warp i: token i; lanes 0-15 hold comb[lane / 4][lane % 4]) ----
+  if (wid < TT) {
+    const int i = wid;
+    const float rsq = rsqrtf(tot[i][kBndStats] / float(FD) + rms_eps);
+    if (lane < 4) {
+      const float m0 = (tot[i][lane] + tot[i][24 + lane]) * rsq;
+      const float m1 = (tot[i][4 + lane] + tot[i][28 + lane]) * rsq;
+      coef[i][lane] = 1.f / (1.f + expf(-(m0 * scale[0] + base[lane]))) + hc_eps;
+      coef[i][4 + lane] = 2.f / (1.f + expf(-(m1 * scale[1] + base[4 + lane])));
+    }
+    const int e = lane & 15;
+    float cv = (tot[i][8 + e] + tot[i][32 + e]) * rsq * scale[2] + base[8 + e];
+    float mx = fmaxf(cv, __shfl_xor_sync(0xffffffffu, cv, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    cv = expf(cv - mx);
+    float s = cv + __shfl_xor_sync(0xffffffffu, cv, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    cv = cv / s + hc_eps;
+    s = cv + __shfl_xor_sync(0xffffffffu, cv, 4);             // column sums
+    s += __shfl_xor_sync(0xffffffffu, s, 8);
+    cv /= (s + hc_eps);
+    for (int it = 1; it < iters; ++it) {
+      s = cv + __shfl_xor_sync(0xffffffffu, cv, 1);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      cv /= (s + hc_eps);
+      s = cv + __shfl_xor_sync(0xffffffffu, cv, 4);
+      s += __shfl_xor_sync(0xffffffffu, s, 8);
+      cv /= (s + hc_eps);
+    }
+    if (lane < 16) coef[i][8 + lane] = cv;
+    __syncwarp();
+    const int t = blockIdx.y * TT + i;
+    if (c == 0 && t < T && lane < 24) {
+      const float v = coef[i][lane];
+      if (lane < 4) pre_out[t * 4 + lane] = v;
+      else if (lane < 8) post_out[t * 4 + lane - 4] = v;
+      else comb_out[t * 16 + lane - 8] = v;
+    }
+  }
+  __syncthreads();
+  // ---- D: pre-mix, cluster-wide RMSNorm, bf16 + fp8 outputs ----
+  float av[TT][8];
+#pragma unroll
+  for (int i = 0; i < TT; ++i) {
+    float s2 = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float a = 0.f;
+#pragma unroll
+      for (int s = 0; s < 4; ++s) a += coef[i][s] * xn[i][s][j];
+      av[i][j] = __bfloat162float(__float2bfloat16_rn(a));
+      s2 += av[i][j] * av[i][j];
+    }
+    s2 = warp_sum(act ? s2 : 0.f);
+    if (lane == 0) part[wid][i] = s2;
+  }
+  __syncthreads();
+  if (k < TT) {
+    float v = 0.f;
+#pragma unroll
+    for (int ww = 0; ww < kBndThreads / 32; ++ww) v += part[ww][k];
+    red2[k] = v;
+  }
+  cluster_sync();
+  if (k < TT) {
+    const uint32_t a = smem_u32(&red2[k]);
+    float v = 0.f;
+    for (int cc = 0; cc < kBndCluster; ++cc) {
+      float x;
+      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x) : "r"(mapa_shared(a, uint32_t(cc))));
+      v += x;
+    }
+    nrm[k] = rsqrtf(v / float(D) + rms_eps);
+  }
+  __syncthreads();
+#pragma unroll
+  for (int i = 0; i < TT; ++i) {
+    const int t = blockIdx.y * TT + i;
+    float amax = 0.f;
+    if (act) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        av[i][j] = __bfloat162float(__float2bfloat16_rn(av[i][j] * nrm[i] * w[col + j]));
+        amax = fmaxf(amax, fabsf(av[i][j]));
+      }
+      if (y && t < T) {
+        uint4 o;
+        o.x = pack_bf16x2(av[i][0], av[i][1]); o.y = pack_bf16x2(av[i][2], av[i][3]);
+        o.z = pack_bf16x2(av[i][4], av[i][5]); o.w = pack_bf16x2(av[i][6], av[i][7]);
+        *reinterpret_cast<uint4*>(y + size_t(t) * D + col) = o;
+      }
+    }
+    if (q) {                                                 // 16 threads = one 128-column block
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      const uint32_t sb = ue8m0_for_amax(amax);
+      const float inv = ue8m0_inv(sb);
+      if (act && t < T) {
+        uint2 wq;
+        wq.x = pack_fp8x4(av[i][0] * inv, av[i][1] * inv, av[i][2] * inv, av[i][3] * inv);
+        wq.y = pack_fp8x4(av[i][4] * inv, av[i][5] * inv, av[i][6] * inv, av[i][7] * inv);
+        *reinterpret_cast<uint2*>(q + size_t(t) * D + col) = wq;
+        if ((k & 15) == 0) reinterpret_cast<uint8_t*>(sf)[sf_byte_offset(t, col / 128, row_blocks)] = uint8_t(sb);
+      }
+    }
+  }
+  cluster_sync();                                            // no CTA leaves while a peer still reads its partials
+}
+
+cudaError_t mhc_boundary_small(void* X, int T, int D, const void* out, const float* post_in, const float* comb_in,
+                               const void* fn, const float* base, const float* scale, int iters, float hc_eps,
+                               float rms_eps, const float* w, void* y, void* q, uint32_t* sf, float* pre_out,
+                               float* post_out, float* comb_out, cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  const int Dc = D / kBndCluster;
+  if (D % (kBndCluster * 128) || Dc > kBndThreads * 8 || (out && (!post_in || !comb_in))) return cudaErrorInvalidValue;
+  constexpr int TT = 2;
+  cb::launch_k(mhc_boundary_small_kernel<TT>, dim3(kBndCluster, ceil_div(T, TT)), kBndThreads, 0, s,
+               reinterpret_cast<__nv_bfloat16*>(X), T, D, reinterpret_cast<const __nv_bfloat16*>(out), post_in,
+               comb_in, reinterpret_cast<const __nv_bfloat16*>(fn), base, scale, iters, hc_eps, rms_eps, w,
+               reinterpret_cast<__nv_bfloat16*>(y), reinterpret_cast<uint8_t*>(q), sf, ceil_div(T, 128), pre_out,
+               post_out, comb_out);
   return cudaGetLastError();
 }
 

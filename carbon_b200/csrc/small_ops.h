@@ -35,6 +35,12 @@ cudaError_t mhc_head_coeffs(const float* mix, int ld_mix, const float* sumsq, co
                             int T, int flat_dim, float hc_eps, float rms_eps, float* pre, cudaStream_t s);
 cudaError_t mhc_pre_norm(const void* X, const float* pre, const float* w, int T, int D, float eps, void* y, void* q,
                          uint32_t* sf, const int* rows, cudaStream_t s);
+// Fused decode-size mHC boundary (post-mix of `out` when given, the next sublayer's statistics and coefficients,
+// pre-mix + RMSNorm + bf16 / fp8 outputs); X [T, 4, D] bf16 updated in place; D a multiple of 1024, at most 8192
+cudaError_t mhc_boundary_small(void* X, int T, int D, const void* out, const float* post_in, const float* comb_in,
+                               const void* fn, const float* base, const float* scale, int iters, float hc_eps,
+                               float rms_eps, const float* w, void* y, void* q, uint32_t* sf, float* pre_out,
+                               float* post_out, float* comb_out, cudaStream_t s);
 cudaError_t mhc_post_mix(const void* X, const void* out, const float* post, const float* comb, int T, int D, void* Xn,
                          float* sumsq, cudaStream_t s);
 cudaError_t embed_hc(const void* table, int row_lo, int rows, const int* ids, int T, int D, int hc, void* X,

@@ -393,6 +393,43 @@ class DeepseekModel:
                          cfg.rms_eps, pre, post, comb)
         return pre, post, comb
 
+    def _boundary_fusable(self, X) -> bool:
+        """Decode-sized batches on the GPU (at most 64 rows on this rank) with 4 residual streams run each boundary
+        as one fused kernel (not while tracing: the trace records the intermediate streams)."""
+        D = self.cfg.hidden_size
+        return (self.on_gpu and self.trace is None and not self.cfg.plain_residual and X.shape[0] <= 64 and
+                X.shape[1] == 4 and D % 1024 == 0 and D <= 8192 and self.cfg.sinkhorn_iters >= 1 and
+                getattr(self.layers[0].attn_hc, "fn", None) is not None and self.layers[0].attn_hc.fn.shape[0] == 48)
+
+    def hc_boundary(self, X, pend, hp: HCParams, w):
+        """One fused decode boundary: mix the pending sublayer output ``pend = (out, post, comb)`` into X (in place;
+        None at the first boundary of a step), then the next sublayer's coefficients and its RMSNorm'd input.
+        Returns (h bf16, (fp8 q, sf), post, comb)."""
+        from ..ops._ext import ext
+        from ..ops.quant import empty_sf
+
+        cfg = self.cfg
+        T, _, D = X.shape
+        dev = X.device
+        y = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
+        q = torch.empty(T, D, dtype=torch.float8_e4m3fn, device=dev)
+        sf = empty_sf(T, D, dev)
+        pre = torch.empty(T, 4, device=dev)
+        post = torch.empty(T, 4, device=dev)
+        comb = torch.empty(T, 4, 4, device=dev)
+        out, p_in, c_in = pend if pend is not None else (None, None, None)
+        ext().mhc_boundary_small(X, out.contiguous() if out is not None else None, p_in, c_in, hp.fn, hp.base,
+                                 hp.scale, cfg.sinkhorn_iters, cfg.hc_eps, cfg.rms_eps, w, y, q, sf, pre, post, comb)
+        return y, (q, sf), post, comb
+
+    def _flush(self, X, sumsq, pend):
+        """Apply a pending fused-boundary post-mix (X, its Σx² and no pending output afterwards)."""
+        if pend is None:
+            return X, sumsq, None
+        with region("mhc.post_mix"):
+            X, sumsq = self.post_mix(X, *pend)
+        return X, sumsq, None
+
     def pre_norm(self, X, pre, w, want_fp8: bool):
         """RMSNorm(Σ pre_i X_i)·w -> (bf16 h, (fp8 q, sf) or None)."""
         if not self.on_gpu:
@@ -881,12 +918,19 @@ class DeepseekModel:
             X, sumsq = self.embed_tokens(fb.ids)
         if cfg.engram_layers:
             cache.write_tokens(fb.out_loc, fb.ids)
+        # decode-sized batches run each mHC boundary as one fused kernel; `pend` is then the last sublayer's output
+        # with its post / comb coefficients, mixed into X by the next boundary (or by post_mix before anything else
+        # reads X)
+        fuse = self._boundary_fusable(X)
+        pend = None
         for i in range(cfg.n_layers):
             L = self.layers[i]
             if i == cfg.late_layer_start and fb.is_prefill:
+                X, sumsq, pend = self._flush(X, sumsq, pend)
                 with region("late.enter_tail"):
                     fb, X, sumsq = self._enter_tail(fb, X, sumsq)
             if L.engram is not None:
+                X, sumsq, pend = self._flush(X, sumsq, pend)
                 with region("engram"):
                     X, sumsq = self.engram(i, X, sumsq, fb, cache)
             if cfg.plain_residual:
@@ -897,6 +941,14 @@ class DeepseekModel:
                 with region("norm"):
                     h, hq = self.plain_norm(X, L.ffn_norm, want_fp8=self.on_gpu)
                 X = self.plain_add(X, self.ffn(i, h, hq))
+                continue
+            if fuse:
+                with region("mhc.boundary"):
+                    h, hq, post, comb = self.hc_boundary(X, pend, L.attn_hc, L.attn_norm)
+                a = self.attention(i, h, hq, fb, cache)
+                with region("mhc.boundary"):
+                    h, hq, post, comb = self.hc_boundary(X, (a, post, comb), L.ffn_hc, L.ffn_norm)
+                pend = (self.ffn(i, h, hq), post, comb)
                 continue
             with region("mhc.coeffs"):
                 pre, post, comb = self.hc_coeffs(X, sumsq, L.attn_hc)
@@ -916,6 +968,7 @@ class DeepseekModel:
             with region("mhc.post_mix"):
                 X, sumsq = self.post_mix(X, f, post, comb)
             self._tr(f"{i}.X_ffn", X)
+        X, sumsq, pend = self._flush(X, sumsq, pend)
         with region("head"):
             return self.logits(X, sumsq, fb)
 

@@ -455,3 +455,55 @@ def test_indexer_decode_logits_tcgen05(T, L, H):
         valid = slots[t, :nt] >= 0
         assert torch.isinf(out[t, :nt][~valid]).all() and torch.isinf(out[t, nt:]).all()
         assert rel_err(out[t, :nt][valid], ref[valid]) < 1e-5, t
+
+
+@pytest.mark.parametrize("T", [1, 5, 32, 64])
+@pytest.mark.parametrize("with_out", [False, True])
+@pytest.mark.parametrize("D", [1024, 7168])
+def test_mhc_boundary_fused_matches_separate_kernels(T, with_out, D):
+    """The fused decode boundary (post-mix + statistics + coefficients + pre-norm, one cluster launch) against the
+    four separate kernels it replaces."""
+    from carbon_b200.models.deepseek import make_hc, mhc_mix
+    from carbon_b200.ops.quant import empty_sf, unpack_sf
+
+    e = _ext()
+    torch.manual_seed(21 + T)
+    hp = make_hc(torch.randn(24, 4 * D) * 0.02, torch.randn(24) * 0.5, torch.rand(3) + 0.5, torch.device(DEV))
+    w = (torch.rand(D) + 0.5).to(DEV)
+    X0 = torch.randn(T, 4, D).to(torch.bfloat16).to(DEV)
+    out = torch.randn(T, D).to(torch.bfloat16).to(DEV) if with_out else None
+    post_in = (torch.rand(T, 4) * 2).to(DEV)
+    comb_in = torch.softmax(torch.randn(T, 4, 4), -1).to(DEV)
+    iters, hc_eps, eps = 20, 1e-6, 1e-6
+    # separate kernels
+    Xa = X0.clone()
+    if with_out:
+        sumsq = torch.empty(T, device=DEV)
+        e.mhc_post_mix(Xa, out, post_in, comb_in.view(-1, 16), Xa, sumsq)
+    else:
+        sumsq = Xa.float().pow(2).sum(dim=(1, 2))
+    mix = mhc_mix(Xa.view(T, 4 * D), hp.fn)
+    pre_a, post_a, comb_a = torch.empty(T, 4, device=DEV), torch.empty(T, 4, device=DEV), torch.empty(T, 4, 4, device=DEV)
+    e.mhc_coeffs(mix, sumsq, hp.base, hp.scale, 4 * D, iters, hc_eps, eps, pre_a, post_a, comb_a)
+    ya = torch.empty(T, D, dtype=torch.bfloat16, device=DEV)
+    qa = torch.empty(T, D, dtype=torch.float8_e4m3fn, device=DEV)
+    sfa = empty_sf(T, D, DEV)
+    e.mhc_pre_norm(Xa, pre_a, w, eps, ya, qa, sfa, None)
+    # fused
+    Xb = X0.clone()
+    yb = torch.empty(T, D, dtype=torch.bfloat16, device=DEV)
+    qb = torch.empty(T, D, dtype=torch.float8_e4m3fn, device=DEV)
+    sfb = empty_sf(T, D, DEV)
+    pre_b, post_b, comb_b = torch.empty(T, 4, device=DEV), torch.empty(T, 4, device=DEV), torch.empty(T, 4, 4, device=DEV)
+    e.mhc_boundary_small(Xb, out, post_in if with_out else None, comb_in if with_out else None, hp.fn, hp.base,
+                         hp.scale, iters, hc_eps, eps, w, yb, qb, sfb, pre_b, post_b, comb_b)
+    torch.cuda.synchronize()
+    # the same post-mix arithmetic: equal up to a rare last-bit difference from FMA contraction
+    assert (Xa != Xb).float().mean().item() < 1e-3
+    assert rel_err(Xb, Xa) < 1e-3
+    for a, b in ((pre_a, pre_b), (post_a, post_b), (comb_a, comb_b)):
+        assert torch.allclose(a, b, rtol=1e-4, atol=1e-6), (a - b).abs().max().item()
+    assert rel_err(yb, ya) < 2e-3, rel_err(yb, ya)
+    da = qa.float().cpu() * unpack_sf(sfa.cpu(), T, D).repeat_interleave(128, 1)
+    db = qb.float().cpu() * unpack_sf(sfb.cpu(), T, D).repeat_interleave(128, 1)
+    assert rel_err(db, da) < 2e-2, rel_err(db, da)
