@@ -33,14 +33,18 @@ constexpr int KV_ATOM = KT * 128;      // 4 KB: 32 rows x 64 dims
 // bf16 rows: the gathered atoms go straight into 5 operand stages
 constexpr int STAGES = 5;
 constexpr int KV_STAGE = NAC_MAX * KV_ATOM;
-// fp8 rows: TMA gathers raw row pieces into 4 staging slots; two converter warps expand the value atoms to fp16
-// operand tiles (3 stages).  A slot holds the RoPE atom (fp16, already in the 128B-swizzled operand layout, read by
-// the MMA in place), the CTA's 256 value bytes of every row (two 128-byte boxes) and the 16 scale bytes of every row
-// (one 4-row gather per 128-byte line: row r at F8_SC + (r / 4) * 128 + (r % 4) * 16).
-constexpr int F8_SLOTS = 4, F8_STAGES = 3;
-constexpr int F8_KV_STAGE = 4 * KV_ATOM;
-constexpr int F8_PE = 0, F8_VAL = 4096, F8_SC = 12288, F8_SLOT = 13312;
-constexpr int F8_SC_BOX = 16;
+// fp8 rows (byte layout: values of dims 0..255 | 8 scale bytes + 8 zero | values of dims 256..511 | fp16 RoPE key):
+// each CTA of the pair gathers ONE contiguous piece per row -- CTA 0 bytes [0, 272), CTA 1 bytes [256, row end) --
+// with one TMA gather4 per 4 rows (the TMA unit's cost is per request, so few large pieces beat many 128-byte
+// ones) into 3 staging slots; two converter warps expand the value atoms to fp16 operand tiles in the 128B-swizzled
+// layout (3 stages) and copy CTA 1's fp16 RoPE atom beside them.  In a slot, rows come in groups of four
+// (one gather each) at 128-byte aligned group strides.
+constexpr int F8_SLOTS = 3, F8_STAGES = 3;
+constexpr int F8_KV_STAGE = NAC_MAX * KV_ATOM;
+constexpr int F8_SLOT = 13312;
+constexpr int F8_PITCH0 = 272;                     // CTA 0: values 0..255 + scales
+CB_HOST_DEVICE constexpr int f8_pitch1(int na) { return na == 9 ? 400 : 272; }   // CTA 1: scales + values (+ RoPE)
+CB_HOST_DEVICE constexpr int f8_group(int pitch) { return (4 * pitch + 127) / 128 * 128; }
 // one partial-score exchange buffer: 128 rows x 32 fp32, rows padded to 36 floats so that the eight threads of a
 // quarter warp reading 16 bytes of eight consecutive rows hit eight different 4-bank groups
 constexpr int X_LD = KT + 4;
@@ -148,7 +152,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
 
   const int t = blockIdx.x, hh = int(cluster_ctarank()), split = blockIdx.z;
   const uint32_t peer = uint32_t(hh ^ 1);
-  const bool rope = NA == 9 && hh == 0;      // this CTA owns the RoPE-key atom
+  const bool rope = NA == 9 && hh == (F8 ? 1 : 0);   // this CTA owns the RoPE-key atom
   const int nac = rope ? 5 : 4;
   const int k_begin = split * p.chunk;
   const int k_end = min(p.K, k_begin + p.chunk);
@@ -164,7 +168,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
       mbar_init(&x_full[i], 1); mbar_init(&x_empty[i], 128);
     }
     if (F8)
-      for (int i = 0; i < F8_SLOTS; ++i) { mbar_init(&st_full[i], 1); mbar_init(&st_empty[i], 3); }
+      for (int i = 0; i < F8_SLOTS; ++i) { mbar_init(&st_full[i], 1); mbar_init(&st_empty[i], 2); }
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -179,7 +183,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
     // ---------------- TMA: this CTA's Q atoms once, then its pieces of the gathered KV rows ----------------
     if (lane == 0 && n_tiles > 0) {
       tma_prefetch_desc(&tm_q); tma_prefetch_desc(&tm_kv);
-      if (F8) { tma_prefetch_desc(&tm_sc); if (rope) tma_prefetch_desc(&tm_pe); }
+      if (F8) tma_prefetch_desc(&tm_sc);
       mbar_arrive_expect_tx(q_full, nac * Q_ATOM);
       for (int la = 0; la < nac; ++la) tma_load_3d(sQ + la * Q_ATOM, &tm_q, q_full, atom_of(hh, la) * 64, 0, t);
     }
@@ -196,7 +200,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
       if (lane == 0) {
         ok = (F8 ? mbar_wait(&st_empty[s], ((j / F8_SLOTS) & 1) ^ 1)
                  : mbar_wait(&kv_empty[s], ((j / STAGES) & 1) ^ 1)) ? 1 : 0;
-        if (ok) mbar_arrive_expect_tx(full, F8 ? 8192 + KT * F8_SC_BOX + (rope ? KV_ATOM : 0) : nac * KV_ATOM);
+        if (ok) mbar_arrive_expect_tx(full, F8 ? KT * (hh ? f8_pitch1(NA) : F8_PITCH0) : nac * KV_ATOM);
         else fail(kErrTimeoutEmpty);
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
@@ -206,13 +210,10 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
       const int r0 = __shfl_sync(0xffffffffu, slot, 4 * g), r1 = __shfl_sync(0xffffffffu, slot, 4 * g + 1);
       const int r2 = __shfl_sync(0xffffffffu, slot, 4 * g + 2), r3 = __shfl_sync(0xffffffffu, slot, 4 * g + 3);
       if constexpr (F8) {
-        uint8_t* sl = sST + s * F8_SLOT;
-        if (part < 2)            // value bytes [256 hh + 128 part, +128) of each row
-          tma_gather4(sl + F8_VAL + part * 4096 + g * 512, &tm_kv, full, hh * 256 + part * 128, r0, r1, r2, r3);
-        else if (part == 2)      // scale bytes [512, 528) of the four rows
-          tma_gather4(sl + F8_SC + g * 128, &tm_sc, full, 512, r0, r1, r2, r3);
-        else if (rope)           // fp16 RoPE key, swizzled into the operand layout
-          tma_gather4(sl + F8_PE + g * 512, &tm_pe, full, 0, r0, r1, r2, r3);
+        // one gather4 of this CTA's contiguous piece of four rows (16-bit elements: CTA 1 starts at byte 256)
+        if (part == 0)
+          tma_gather4(sST + s * F8_SLOT + g * f8_group(hh ? f8_pitch1(NA) : F8_PITCH0), hh ? &tm_sc : &tm_kv, full,
+                      hh * 128, r0, r1, r2, r3);
       } else {
         if (part < 4)
           tma_gather4(sKV + s * KV_STAGE + part * KV_ATOM + g * 4 * 128, &tm_kv, full, atom_of(hh, part) * 64, r0, r1,
@@ -237,14 +238,16 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
       if (!ok || *abort_flag) break;
       const uint8_t* sl = sST + s8 * F8_SLOT;
       uint8_t* dst = sKV + s * F8_KV_STAGE;
+      const int pitch = hh ? f8_pitch1(NA) : F8_PITCH0, grp = f8_group(pitch);
+      const int voff = hh ? 16 : 0, soff = hh ? 0 : 256;      // values / scale bytes within this CTA's piece
 #pragma unroll 2
       for (int i = 0; i < 8; ++i) {
-        // task: row, local atom la, 16-value chunk c; a warp's 32 lanes read four whole 128-byte row pieces
+        // task: row, local atom la, 16-value chunk c (a warp's lanes cover two rows' 256 value bytes)
         const int id = cw * 256 + i * 32 + int(lane);
         const int row = id >> 4, la = (id >> 2) & 3, c = id & 3;
-        const uint4 v = *reinterpret_cast<const uint4*>(sl + F8_VAL + (la >> 1) * 4096 + row * 128 + (la & 1) * 64 +
-                                                        c * 16);
-        const uint32_t sb = sl[F8_SC + (row >> 2) * 128 + (row & 3) * F8_SC_BOX + hh * 4 + la];
+        const uint8_t* rp = sl + (row >> 2) * grp + (row & 3) * pitch;
+        const uint4 v = *reinterpret_cast<const uint4*>(rp + voff + la * 64 + c * 16);
+        const uint32_t sb = rp[soff + hh * 4 + la];
         const __half hs = __float2half_rn(ue8m0_to_float(sb));
         const uint32_t s2 = uint32_t(*reinterpret_cast<const uint16_t*>(&hs)) * 0x10001u;
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -259,6 +262,15 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
         *reinterpret_cast<uint4*>(rowp + (((2 * c) ^ sw) << 4)) = make_uint4(h[0], h[1], h[2], h[3]);
         *reinterpret_cast<uint4*>(rowp + (((2 * c + 1) ^ sw) << 4)) = make_uint4(h[4], h[5], h[6], h[7]);
       }
+      if (rope) {                            // fp16 RoPE key (bytes 272..399 of CTA 1's piece) -> operand atom 4
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int id = cw * 128 + i * 32 + int(lane);
+          const int row = id >> 3, c8 = id & 7;
+          const uint4 v = *reinterpret_cast<const uint4*>(sl + (row >> 2) * grp + (row & 3) * pitch + 272 + c8 * 16);
+          *reinterpret_cast<uint4*>(dst + 4 * KV_ATOM + row * 128 + ((c8 ^ (row & 7)) << 4)) = v;
+        }
+      }
       fence_proxy_async();                   // generic-proxy stores -> visible to the tensor core's operand reads
       __syncwarp();
       if (lane == 0) { mbar_arrive(&kv_full[s]); mbar_arrive(&st_empty[s8]); }
@@ -271,19 +283,17 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
       bool ok = mbar_wait(q_full, 0);
       if (!ok) fail(kErrTimeoutFull);
       auto issue_qk = [&](int j) -> bool {
-        const int s = j % NST, b = j & 1, s8 = j % F8_SLOTS;
+        const int s = j % NST, b = j & 1;
         if (!mbar_wait(&kv_full[s], (j / NST) & 1)) { fail(kErrTimeoutFull); return false; }
-        if (F8 && rope && !mbar_wait(&st_full[s8], (j / F8_SLOTS) & 1)) { fail(kErrTimeoutFull); return false; }
         tc_fence_after();
         for (int la = 0; la < nac; ++la) {
-          const uint8_t* kb = (F8 && la == 4) ? sST + s8 * F8_SLOT + F8_PE : sKV + s * STAGE_B + la * KV_ATOM;
+          const uint8_t* kb = sKV + s * STAGE_B + la * KV_ATOM;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
             mma_f16_ss(tmem + TM_S + b * TM_S_STRIDE, smem_desc_sw128(sQ + la * Q_ATOM + kk * 32),
                        smem_desc_sw128(kb + kk * 32), id_qk, (la | kk) > 0);
         }
         mma_commit(&s_full[b]);
-        if (F8) mma_commit(&st_empty[s8]);   // the slot's RoPE atom has been read
         return true;
       };
       auto issue_pv = [&](int j) -> bool {
@@ -478,7 +488,8 @@ __global__ void mla_combine_kernel(const float* __restrict__ part_o, const float
 // fp8 latent rows.  A cached token row of the fp8 format holds r = 512 e4m3 latent values quantised per 64-dim atom
 // (UE8M0 power-of-two scale, the smallest 2^e with amax / 2^e <= 448), the 8 scale bytes padded to 16, and for MLA
 // the 64 RoPE-key dims as fp16: 656 bytes per MLA token (1152 in bf16), 528 per latent-MQA token (its RoPE dims are
-// the last latent atom).  One warp per row: lane l quantises dims [16 l, 16 l + 16), lanes 4a..4a+3 form atom a.
+// the last latent atom).  Byte layout: values of dims 0..255 | scales | values of dims 256..511 | RoPE key.
+// One warp per row: lane l quantises dims [16 l, 16 l + 16), lanes 4a..4a+3 form atom a.
 // ---------------------------------------------------------------------------------------------------------------
 __global__ void latent_store_fp8_kernel(const __nv_bfloat16* __restrict__ rows, int n, int ld, int D,
                                         const int* __restrict__ slots, uint8_t* __restrict__ cache, int RB) {
@@ -507,15 +518,15 @@ __global__ void latent_store_fp8_kernel(const __nv_bfloat16* __restrict__ rows, 
   q.y = pack_fp8x4(v[4] * inv, v[5] * inv, v[6] * inv, v[7] * inv);
   q.z = pack_fp8x4(v[8] * inv, v[9] * inv, v[10] * inv, v[11] * inv);
   q.w = pack_fp8x4(v[12] * inv, v[13] * inv, v[14] * inv, v[15] * inv);
-  reinterpret_cast<uint4*>(dst)[lane] = q;
-  // scale bytes of atoms 0..7 (lanes 0, 4, ..., 28) -> bytes [512, 528), the last 8 zero
+  *reinterpret_cast<uint4*>(dst + lane * 16 + (lane >= 16 ? 16 : 0)) = q;   // dims 256.. follow the scale bytes
+  // scale bytes of atoms 0..7 (lanes 0, 4, ..., 28) -> bytes [256, 272), the last 8 zero
   uint32_t lo = 0, hi = 0;
 #pragma unroll
   for (int a = 0; a < 8; ++a) {
     const uint32_t b = __shfl_sync(0xffffffffu, sb, 4 * a);
     if (a < 4) lo |= b << (8 * a); else hi |= b << (8 * (a - 4));
   }
-  if (lane == 0) *reinterpret_cast<uint4*>(dst + 512) = make_uint4(lo, hi, 0u, 0u);
+  if (lane == 0) *reinterpret_cast<uint4*>(dst + 256) = make_uint4(lo, hi, 0u, 0u);
   if (D == 576 && lane < 16) {                            // RoPE key dims 512..575 -> fp16 at bytes [528, 656)
     const uint2 r2 = *reinterpret_cast<const uint2*>(x + 512 + lane * 4);
     __half2 h0 = __floats2half2_rn(bf16_lo(r2.x), bf16_hi(r2.x));
@@ -599,22 +610,16 @@ cudaError_t sparse_mla_any(bool f8, const void* q, int T, int H, const void* kv,
     tsc = tkv;
     tpe = tkv;
   } else {
-    const cuuint64_t dims[2] = {cuuint64_t(RB), cuuint64_t(S)};
+    // 16-bit elements over each row: CTA 0 reads [0, 272) bytes, CTA 1 [256, RB)
+    const cuuint64_t dims[2] = {cuuint64_t(RB / 2), cuuint64_t(S)};
     const cuuint64_t str[1] = {cuuint64_t(RB)};
-    const cuuint32_t box_v[2] = {128, 1}, box_s[2] = {uint32_t(F8_SC_BOX), 1};
-    if (make_map(&tkv, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, kv, dims, str, box_v, CU_TENSOR_MAP_SWIZZLE_NONE) !=
+    const cuuint32_t box0[2] = {F8_PITCH0 / 2, 1}, box1[2] = {uint32_t(RB - 256) / 2, 1};
+    if (make_map(&tkv, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, kv, dims, str, box0, CU_TENSOR_MAP_SWIZZLE_NONE) !=
             CUDA_SUCCESS ||
-        make_map(&tsc, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, kv, dims, str, box_s, CU_TENSOR_MAP_SWIZZLE_NONE) !=
+        make_map(&tsc, CU_TENSOR_MAP_DATA_TYPE_UINT16, 2, kv, dims, str, box1, CU_TENSOR_MAP_SWIZZLE_NONE) !=
             CUDA_SUCCESS)
       return cudaErrorInvalidValue;
     tpe = tkv;
-    if (D == 576) {                                            // fp16 RoPE key at bytes [528, 656) of each row
-      const cuuint64_t dpe[2] = {64, cuuint64_t(S)};
-      const cuuint32_t box_pe[2] = {64, 1};
-      if (make_map(&tpe, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, static_cast<const uint8_t*>(kv) + 528, dpe, str, box_pe,
-                   CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
-        return cudaErrorInvalidValue;
-    }
   }
   Params p;
   p.idx = idx; p.K = K; p.H = H; p.n_splits = n_splits;

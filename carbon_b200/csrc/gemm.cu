@@ -146,45 +146,48 @@ __global__ void splitk_reduce_out_kernel(const float* __restrict__ part, int spl
 }
 
 // Split-K partials of an interleaved gate/up GEMM (N = 2I, 128-column chunks gate|up) -> SwiGLU -> fp8 + SF tiles,
-// exactly the SwiGLU epilogue's arithmetic.  One warp per (row, 128 output columns), 4 outputs per lane.
+// exactly the SwiGLU epilogue's arithmetic.  One warp per (row, 128 output columns), 4 outputs per lane; warps
+// stride over the work (a grouped call's row count is only known on the device: n_blocks * 128 rows, so the grid is
+// sized for the SMs, not for the padded capacity).
 __global__ void splitk_reduce_swiglu_kernel(const float* __restrict__ part, int splits, int M, int N, float limit,
                                             uint8_t* __restrict__ out, int ldo, uint32_t* __restrict__ out_sf,
                                             int sf_row_blocks, const int* __restrict__ row_valid,
                                             const int* __restrict__ n_blocks) {
   cb::pdl_entry();
   const int I = N / 2, chunks = I / 128;
-  const int wg = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (wg >= M * chunks) return;
-  const int row = wg / chunks, g = wg % chunks;
-  if (n_blocks && row >= n_blocks[0] * 128) return;
-  if (row_valid && row_valid[row] < 0) return;     // padding rows of an expert segment: never read back
-  float a[4];
-  float amax = 0.f;
+  const int rows = n_blocks ? min(M, n_blocks[0] * 128) : M;
+  const int nw = gridDim.x * (blockDim.x >> 5);
+  for (int wg = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); wg < rows * chunks; wg += nw) {
+    const int row = wg / chunks, g = wg % chunks;
+    if (row_valid && row_valid[row] < 0) continue;  // padding rows of an expert segment: never read back
+    float a[4];
+    float amax = 0.f;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int t = 4 * lane + i;
-    float gv = 0.f, uv = 0.f;
-    for (int sp = 0; sp < splits; ++sp) {
-      const float* pr = part + (size_t(sp) * M + row) * N + 256 * g;
-      gv += pr[t];
-      uv += pr[128 + t];
+    for (int i = 0; i < 4; ++i) {
+      const int t = 4 * lane + i;
+      float gv = 0.f, uv = 0.f;
+      for (int sp = 0; sp < splits; ++sp) {
+        const float* pr = part + (size_t(sp) * M + row) * N + 256 * g;
+        gv += pr[t];
+        uv += pr[128 + t];
+      }
+      if (limit > 0.f) { gv = fminf(gv, limit); uv = fminf(fmaxf(uv, -limit), limit); }
+      a[i] = gv / (1.f + __expf(-gv)) * uv;
+      amax = fmaxf(amax, fabsf(a[i]));
     }
-    if (limit > 0.f) { gv = fminf(gv, limit); uv = fminf(fmaxf(uv, -limit), limit); }
-    a[i] = gv / (1.f + __expf(-gv)) * uv;
-    amax = fmaxf(amax, fabsf(a[i]));
-  }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-  const uint32_t sb = ue8m0_for_amax(amax);
-  const float inv = ue8m0_inv(sb);
-  *reinterpret_cast<uint32_t*>(out + size_t(row) * ldo + 128 * g + 4 * lane) =
-      pack_fp8x4(a[0] * inv, a[1] * inv, a[2] * inv, a[3] * inv);
-  if (lane == 0) {
-    const int rb = row / 128, r = row % 128;
-    uint8_t* sf = reinterpret_cast<uint8_t*>(out_sf) +
-                  ((size_t(g >> 2) * sf_row_blocks + rb) * 128 + (r % 32) * 4 + (r / 32)) * 4 + (g & 3);
-    *sf = uint8_t(sb);
+    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const uint32_t sb = ue8m0_for_amax(amax);
+    const float inv = ue8m0_inv(sb);
+    *reinterpret_cast<uint32_t*>(out + size_t(row) * ldo + 128 * g + 4 * lane) =
+        pack_fp8x4(a[0] * inv, a[1] * inv, a[2] * inv, a[3] * inv);
+    if (lane == 0) {
+      const int rb = row / 128, r = row % 128;
+      uint8_t* sf = reinterpret_cast<uint8_t*>(out_sf) +
+                    ((size_t(g >> 2) * sf_row_blocks + rb) * 128 + (r % 32) * 4 + (r / 32)) * 4 + (g & 3);
+      *sf = uint8_t(sb);
+    }
   }
 }
 
@@ -277,7 +280,8 @@ cudaError_t gemm_fp8(const void* A, const void* B, const uint32_t* sfa, const ui
       cudaError_t e = launch<KIND_MXF8, EPI_F32, 128, 6, 2>(ta, tb, p, max_tiles, num_sms, s);
       if (e != cudaSuccess) return e;
       const int warps = M * (N / 256);
-      cb::launch_k(splitk_reduce_swiglu_kernel, ceil_div(warps, 8), 256, 0, s, work, 1, M, N, swiglu_limit,
+      cb::launch_k(splitk_reduce_swiglu_kernel, min(ceil_div(warps, 8), num_sms * 8), 256, 0, s, work, 1, M, N,
+                   swiglu_limit,
                                                                      reinterpret_cast<uint8_t*>(out), ldo, out_sf,
                                                                      ceil_div(M, 128), row_valid, num_m_blocks_dev);
       return cudaGetLastError();
@@ -307,7 +311,8 @@ cudaError_t gemm_fp8(const void* A, const void* B, const uint32_t* sfa, const ui
     const int used = ceil_div(nk_total, nk_per);
     if (epi == GEMM_OUT_SWIGLU_FP8) {
       const int warps = M * (N / 256);
-      cb::launch_k(splitk_reduce_swiglu_kernel, ceil_div(warps, 8), 256, 0, s, work, used, M, N, swiglu_limit,
+      cb::launch_k(splitk_reduce_swiglu_kernel, min(ceil_div(warps, 8), num_sms * 8), 256, 0, s, work, used, M, N,
+                   swiglu_limit,
                                                                      reinterpret_cast<uint8_t*>(out), ldo, out_sf,
                                                                      ceil_div(M, 128), nullptr, nullptr);
     } else {

@@ -231,28 +231,30 @@ cudaError_t sf_pad(uint32_t* sf, int M, int K, cudaStream_t s) {
 // RoPE (interleaved pairs) in place on bf16 x[T, H, *] at column offset `off`, width `dim`.
 // cos_sin: fp32 [max_pos, dim] laid out as (cos_0, sin_0, cos_1, sin_1, ...).
 // ---------------------------------------------------------------------------------------------------------------
+// RoPE in place on dims [off, off + dim) of every head (interleaved pairs).  Grid (T, ceil(H / 4)): a CTA rotates 4
+// heads of one token, one pair per thread (dim <= 64), so decode-sized calls spread over many SMs.
 __global__ void rope_kernel(__nv_bfloat16* x, int64_t stride_t, int64_t stride_h, int H, int off, int dim,
                             const float* __restrict__ cos_sin, const int* __restrict__ pos, int inverse) {
   cb::pdl_entry();
   const int t = blockIdx.x;
   const int p = pos[t];
   const int pairs = dim / 2;
-  for (int i = threadIdx.x; i < H * pairs; i += blockDim.x) {
-    const int h = i / pairs, j = i - h * pairs;
-    __nv_bfloat16* e = x + t * stride_t + h * stride_h + off + 2 * j;
-    const float c = cos_sin[size_t(p) * dim + 2 * j];
-    float sn = cos_sin[size_t(p) * dim + 2 * j + 1];
-    if (inverse) sn = -sn;
-    const float a = __bfloat162float(e[0]), b = __bfloat162float(e[1]);
-    e[0] = __float2bfloat16_rn(a * c - b * sn);
-    e[1] = __float2bfloat16_rn(a * sn + b * c);
+  for (int i = threadIdx.x; i < 4 * pairs; i += blockDim.x) {
+    const int h = blockIdx.y * 4 + i / pairs, j = i % pairs;
+    if (h >= H) break;
+    __nv_bfloat162* e = reinterpret_cast<__nv_bfloat162*>(x + t * stride_t + h * stride_h + off + 2 * j);
+    const float2 cs = *reinterpret_cast<const float2*>(cos_sin + size_t(p) * dim + 2 * j);
+    const float c = cs.x, sn = inverse ? -cs.y : cs.y;
+    const float2 ab = __bfloat1622float2(*e);
+    *e = __floats2bfloat162_rn(ab.x * c - ab.y * sn, ab.x * sn + ab.y * c);
   }
 }
 cudaError_t rope_inplace(void* x, int T, int64_t stride_t, int64_t stride_h, int H, int off, int dim,
                          const float* cos_sin, const int* pos, bool inverse, cudaStream_t s) {
   if (T == 0) return cudaSuccess;
-  cb::launch_k(rope_kernel, T, 128, 0, s, reinterpret_cast<__nv_bfloat16*>(x), stride_t, stride_h, H, off, dim, cos_sin, pos,
-                                inverse ? 1 : 0);
+  if ((off | dim | stride_t | stride_h) & 1) return cudaErrorInvalidValue;     // bf16 pairs are 4-byte aligned
+  cb::launch_k(rope_kernel, dim3(T, ceil_div(H, 4)), 128, 0, s, reinterpret_cast<__nv_bfloat16*>(x), stride_t,
+               stride_h, H, off, dim, cos_sin, pos, inverse ? 1 : 0);
   return cudaGetLastError();
 }
 
@@ -490,7 +492,7 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ Y, int ldy,
                                    __nv_bfloat16* __restrict__ out, int D) {
   cb::pdl_entry();
   const int t = blockIdx.x;
-  for (int c = threadIdx.x * 8; c < D; c += blockDim.x * 8) {
+  for (int c = (blockIdx.y * blockDim.x + threadIdx.x) * 8; c < D; c += gridDim.y * blockDim.x * 8) {
     float acc[8];
     if (add) {
       uint4 raw = *reinterpret_cast<const uint4*>(add + size_t(t) * D + c);
@@ -519,7 +521,7 @@ cudaError_t moe_combine(const void* Y, int ldy, const float* w, const int* slot_
                         void* out, int D, cudaStream_t s) {
   if (T == 0) return cudaSuccess;
   if (D % 8) return cudaErrorInvalidValue;
-  cb::launch_k(moe_combine_kernel, T, 128, 0, s, reinterpret_cast<const __nv_bfloat16*>(Y), ldy, w, slot_pos, k,
+  cb::launch_k(moe_combine_kernel, dim3(T, ceil_div(D, 128 * 8)), 128, 0, s, reinterpret_cast<const __nv_bfloat16*>(Y), ldy, w, slot_pos, k,
                                        reinterpret_cast<const __nv_bfloat16*>(add),
                                        reinterpret_cast<__nv_bfloat16*>(out), D);
   return cudaGetLastError();
@@ -829,8 +831,10 @@ cudaError_t mhc_post_mix(const void* X, const void* out, const float* post, cons
 // summation order of the reductions differs.  Reference role: the Mega-mHC boundary kernel of the reference
 // (king_v10/bundle_v9/cuda_moe_prefill.py:862 sm100_mega_mhc; decode use in dec/prenorm_pair.py).
 // ---------------------------------------------------------------------------------------------------------------
-constexpr int kBndCluster = 8, kBndThreads = 128, kBndStats = 48;
+constexpr int kBndCluster = 8, kBndCols = 128, kBndThreads = 4 * kBndCols, kBndStats = 48, kBndWarps = kBndThreads / 32;
 
+// Thread (k, g): column chunk k (8 columns) of this CTA's range and residual stream g.  Phase A gives each thread
+// its stream's new values; phases B (statistics) and D (pre-mix over the 4 streams, from shared memory) follow.
 template <int TT>
 __global__ void __cluster_dims__(kBndCluster, 1, 1) __launch_bounds__(kBndThreads)
     mhc_boundary_small_kernel(__nv_bfloat16* X, int T, int D, const __nv_bfloat16* __restrict__ out,
@@ -841,7 +845,8 @@ __global__ void __cluster_dims__(kBndCluster, 1, 1) __launch_bounds__(kBndThread
                               uint32_t* __restrict__ sf, int row_blocks, float* __restrict__ pre_out,
                               float* __restrict__ post_out, float* __restrict__ comb_out) {
   cb::pdl_entry();
-  __shared__ float part[kBndThreads / 32][TT * 8];           // per-warp partials of one 8-row group
+  __shared__ float xs_sm[TT][4][kBndCols * 8];                // the new streams of this CTA's columns
+  __shared__ float part[kBndWarps][TT * 8];                   // per-warp partials of one 8-row group
   __shared__ float red[TT][kBndStats + 1];                    // this CTA's stats partials + Σx² (read cluster-wide)
   __shared__ float tot[TT][kBndStats + 1];
   __shared__ float coef[TT][24];                              // pre[4], post[4], comb[16]
@@ -849,69 +854,65 @@ __global__ void __cluster_dims__(kBndCluster, 1, 1) __launch_bounds__(kBndThread
   __shared__ float nrm[TT];
   const int c = int(cluster_ctarank());
   const int Dc = D / kBndCluster;
-  const int k = threadIdx.x, lane = k & 31, wid = k >> 5;
+  const int k = threadIdx.x % kBndCols, g = threadIdx.x / kBndCols;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
   const bool act = k * 8 < Dc;
   const int col = c * Dc + k * 8;
   const size_t FD = size_t(4) * D;
-  float xn[TT][4][8];
+  float xg[TT][8];                                            // stream g of this thread's 8 columns, per token
   float ss[TT];
-  // ---- A: post-mix (or plain read) ----
+  // ---- A: post-mix of stream g (or plain read) ----
 #pragma unroll
   for (int i = 0; i < TT; ++i) {
     const int t = blockIdx.y * TT + i;
+    const bool live = act && t < T;
+    __nv_bfloat16* xr = X + size_t(live ? t : 0) * FD;
     ss[i] = 0.f;
 #pragma unroll
-    for (int s = 0; s < 4; ++s)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) xn[i][s][j] = 0.f;
-    if (!act || t >= T) continue;
-    __nv_bfloat16* xr = X + size_t(t) * FD;
-    float xs[4][8];
-#pragma unroll
-    for (int s = 0; s < 4; ++s) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(xr + size_t(s) * D + col);
-      xs[s][0] = bf16_lo(raw.x); xs[s][1] = bf16_hi(raw.x); xs[s][2] = bf16_lo(raw.y); xs[s][3] = bf16_hi(raw.y);
-      xs[s][4] = bf16_lo(raw.z); xs[s][5] = bf16_hi(raw.z); xs[s][6] = bf16_lo(raw.w); xs[s][7] = bf16_hi(raw.w);
-    }
+    for (int j = 0; j < 8; ++j) xg[i][j] = 0.f;
     if (out) {
-      float ov[8];
-      const uint4 r0 = *reinterpret_cast<const uint4*>(out + size_t(t) * D + col);
-      ov[0] = bf16_lo(r0.x); ov[1] = bf16_hi(r0.x); ov[2] = bf16_lo(r0.y); ov[3] = bf16_hi(r0.y);
-      ov[4] = bf16_lo(r0.z); ov[5] = bf16_hi(r0.z); ov[6] = bf16_lo(r0.w); ov[7] = bf16_hi(r0.w);
-      float pst[4], cbm[16];
+      if (live) {
+        float xs[4][8], ov[8];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) pst[j] = post_in[t * 4 + j];
+        for (int s = 0; s < 4; ++s) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(xr + size_t(s) * D + col);
+          xs[s][0] = bf16_lo(raw.x); xs[s][1] = bf16_hi(raw.x); xs[s][2] = bf16_lo(raw.y); xs[s][3] = bf16_hi(raw.y);
+          xs[s][4] = bf16_lo(raw.z); xs[s][5] = bf16_hi(raw.z); xs[s][6] = bf16_lo(raw.w); xs[s][7] = bf16_hi(raw.w);
+        }
+        const uint4 r0 = *reinterpret_cast<const uint4*>(out + size_t(t) * D + col);
+        ov[0] = bf16_lo(r0.x); ov[1] = bf16_hi(r0.x); ov[2] = bf16_lo(r0.y); ov[3] = bf16_hi(r0.y);
+        ov[4] = bf16_lo(r0.z); ov[5] = bf16_hi(r0.z); ov[6] = bf16_lo(r0.w); ov[7] = bf16_hi(r0.w);
+        const float pst = post_in[t * 4 + g];
+        float cbm[4];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) cbm[j] = comb_in[t * 16 + j];
-#pragma unroll
-      for (int o = 0; o < 4; ++o) {
+        for (int ii = 0; ii < 4; ++ii) cbm[ii] = comb_in[t * 16 + ii * 4 + g];
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          float a = pst[o] * ov[j];
+          float a = pst * ov[j];
 #pragma unroll
-          for (int ii = 0; ii < 4; ++ii) a += cbm[ii * 4 + o] * xs[ii][j];
-          xn[i][o][j] = __bfloat162float(__float2bfloat16_rn(a));
+          for (int ii = 0; ii < 4; ++ii) a += cbm[ii] * xs[ii][j];
+          xg[i][j] = __bfloat162float(__float2bfloat16_rn(a));
         }
       }
-#pragma unroll
-      for (int o = 0; o < 4; ++o) {
+      __syncthreads();                       // every stream of these columns is read before any thread writes one
+      if (live) {
         uint4 wv;
-        wv.x = pack_bf16x2(xn[i][o][0], xn[i][o][1]); wv.y = pack_bf16x2(xn[i][o][2], xn[i][o][3]);
-        wv.z = pack_bf16x2(xn[i][o][4], xn[i][o][5]); wv.w = pack_bf16x2(xn[i][o][6], xn[i][o][7]);
-        *reinterpret_cast<uint4*>(xr + size_t(o) * D + col) = wv;
+        wv.x = pack_bf16x2(xg[i][0], xg[i][1]); wv.y = pack_bf16x2(xg[i][2], xg[i][3]);
+        wv.z = pack_bf16x2(xg[i][4], xg[i][5]); wv.w = pack_bf16x2(xg[i][6], xg[i][7]);
+        *reinterpret_cast<uint4*>(xr + size_t(g) * D + col) = wv;
       }
-    } else {
-#pragma unroll
-      for (int s = 0; s < 4; ++s)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) xn[i][s][j] = xs[s][j];
+    } else if (live) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(xr + size_t(g) * D + col);
+      xg[i][0] = bf16_lo(raw.x); xg[i][1] = bf16_hi(raw.x); xg[i][2] = bf16_lo(raw.y); xg[i][3] = bf16_hi(raw.y);
+      xg[i][4] = bf16_lo(raw.z); xg[i][5] = bf16_hi(raw.z); xg[i][6] = bf16_lo(raw.w); xg[i][7] = bf16_hi(raw.w);
     }
 #pragma unroll
-    for (int s = 0; s < 4; ++s)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) ss[i] += xn[i][s][j] * xn[i][s][j];
+    for (int j = 0; j < 8; ++j) {
+      ss[i] += xg[i][j] * xg[i][j];
+      xs_sm[i][g][k * 8 + j] = xg[i][j];
+    }
   }
-  // ---- B: statistics partials over this CTA's columns, 8 fn rows at a time ----
+  // ---- B: statistics partials over this CTA's columns of stream g, 8 fn rows at a time ----
   for (int r0 = 0; r0 < kBndStats; r0 += 8) {
     float acc[TT][8];
 #pragma unroll
@@ -919,19 +920,18 @@ __global__ void __cluster_dims__(kBndCluster, 1, 1) __launch_bounds__(kBndThread
 #pragma unroll
       for (int rr = 0; rr < 8; ++rr) acc[i][rr] = 0.f;
     if (act) {
+      uint4 fv[8];
+#pragma unroll
+      for (int rr = 0; rr < 8; ++rr)
+        fv[rr] = __ldg(reinterpret_cast<const uint4*>(fn + size_t(r0 + rr) * FD + size_t(g) * D + col));
 #pragma unroll
       for (int rr = 0; rr < 8; ++rr) {
-        const __nv_bfloat16* fr = fn + size_t(r0 + rr) * FD + col;
+        const float f[8] = {bf16_lo(fv[rr].x), bf16_hi(fv[rr].x), bf16_lo(fv[rr].y), bf16_hi(fv[rr].y),
+                            bf16_lo(fv[rr].z), bf16_hi(fv[rr].z), bf16_lo(fv[rr].w), bf16_hi(fv[rr].w)};
 #pragma unroll
-        for (int s = 0; s < 4; ++s) {
-          const uint4 fv = __ldg(reinterpret_cast<const uint4*>(fr + size_t(s) * D));
-          const float f[8] = {bf16_lo(fv.x), bf16_hi(fv.x), bf16_lo(fv.y), bf16_hi(fv.y),
-                              bf16_lo(fv.z), bf16_hi(fv.z), bf16_lo(fv.w), bf16_hi(fv.w)};
+        for (int i = 0; i < TT; ++i)
 #pragma unroll
-          for (int i = 0; i < TT; ++i)
-#pragma unroll
-            for (int j = 0; j < 8; ++j) acc[i][rr] += xn[i][s][j] * f[j];
-        }
+          for (int j = 0; j < 8; ++j) acc[i][rr] += xg[i][j] * f[j];
       }
     }
 #pragma unroll
@@ -942,11 +942,11 @@ __global__ void __cluster_dims__(kBndCluster, 1, 1) __launch_bounds__(kBndThread
         if (lane == 0) part[wid][i * 8 + rr] = v;
       }
     __syncthreads();
-    if (k < TT * 8) {
+    if (threadIdx.x < TT * 8) {
       float v = 0.f;
 #pragma unroll
-      for (int ww = 0; ww < kBndThreads / 32; ++ww) v += part[ww][k];
-      red[k / 8][r0 + k % 8] = v;
+      for (int ww = 0; ww < kBndWarps; ++ww) v += part[ww][threadIdx.x];
+      red[threadIdx.x / 8][r0 + threadIdx.x % 8] = v;
     }
     __syncthreads();
   }
@@ -956,16 +956,17 @@ __global__ void __cluster_dims__(kBndCluster, 1, 1) __launch_bounds__(kBndThread
     if (lane == 0) part[wid][i] = v;
   }
   __syncthreads();
-  if (k < TT) {
+  if (threadIdx.x < TT) {
     float v = 0.f;
 #pragma unroll
-    for (int ww = 0; ww < kBndThreads / 32; ++ww) v += part[ww][k];
-    red[k][kBndStats] = v;
+    for (int ww = 0; ww < kBndWarps; ++ww) v += part[ww][threadIdx.x];
+    red[threadIdx.x][kBndStats] = v;
   }
   cluster_sync();                                            // every CTA's partials are visible cluster-wide
-  for (int e = k; e < TT * (kBndStats + 1); e += kBndThreads) {
+  for (int e = threadIdx.x; e < TT * (kBndStats + 1); e += kBndThreads) {
     const uint32_t a = smem_u32(&red[0][0] + e);
     float v = 0.f;
+#pragma unroll
     for (int cc = 0; cc < kBndCluster; ++cc) {
       float x;
       asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x) : "r"(mapa_shared(a, uint32_t(cc))));
@@ -1014,55 +1015,55 @@ __global__ void __cluster_dims__(kBndCluster, 1, 1) __launch_bounds__(kBndThread
     }
   }
   __syncthreads();
-  // ---- D: pre-mix, cluster-wide RMSNorm, bf16 + fp8 outputs ----
-  float av[TT][8];
-#pragma unroll
-  for (int i = 0; i < TT; ++i) {
+  // ---- D: pre-mix of the 4 streams (thread group g < TT: token g), cluster-wide RMSNorm, bf16 + fp8 outputs ----
+  const int it = g;                                          // token of this thread group in phase D
+  float av[8];
+  if (it < TT) {
     float s2 = 0.f;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       float a = 0.f;
 #pragma unroll
-      for (int s = 0; s < 4; ++s) a += coef[i][s] * xn[i][s][j];
-      av[i][j] = __bfloat162float(__float2bfloat16_rn(a));
-      s2 += av[i][j] * av[i][j];
+      for (int s = 0; s < 4; ++s) a += coef[it][s] * xs_sm[it][s][k * 8 + j];
+      av[j] = __bfloat162float(__float2bfloat16_rn(a));
+      s2 += av[j] * av[j];
     }
     s2 = warp_sum(act ? s2 : 0.f);
-    if (lane == 0) part[wid][i] = s2;
+    if (lane == 0) part[wid][0] = s2;
   }
   __syncthreads();
-  if (k < TT) {
+  if (threadIdx.x < TT) {
     float v = 0.f;
 #pragma unroll
-    for (int ww = 0; ww < kBndThreads / 32; ++ww) v += part[ww][k];
-    red2[k] = v;
+    for (int ww = 0; ww < kBndCols / 32; ++ww) v += part[threadIdx.x * (kBndCols / 32) + ww][0];
+    red2[threadIdx.x] = v;
   }
   cluster_sync();
-  if (k < TT) {
-    const uint32_t a = smem_u32(&red2[k]);
+  if (threadIdx.x < TT) {
+    const uint32_t a = smem_u32(&red2[threadIdx.x]);
     float v = 0.f;
+#pragma unroll
     for (int cc = 0; cc < kBndCluster; ++cc) {
       float x;
       asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x) : "r"(mapa_shared(a, uint32_t(cc))));
       v += x;
     }
-    nrm[k] = rsqrtf(v / float(D) + rms_eps);
+    nrm[threadIdx.x] = rsqrtf(v / float(D) + rms_eps);
   }
   __syncthreads();
-#pragma unroll
-  for (int i = 0; i < TT; ++i) {
-    const int t = blockIdx.y * TT + i;
+  if (it < TT) {
+    const int t = blockIdx.y * TT + it;
     float amax = 0.f;
     if (act) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        av[i][j] = __bfloat162float(__float2bfloat16_rn(av[i][j] * nrm[i] * w[col + j]));
-        amax = fmaxf(amax, fabsf(av[i][j]));
+        av[j] = __bfloat162float(__float2bfloat16_rn(av[j] * nrm[it] * w[col + j]));
+        amax = fmaxf(amax, fabsf(av[j]));
       }
       if (y && t < T) {
         uint4 o;
-        o.x = pack_bf16x2(av[i][0], av[i][1]); o.y = pack_bf16x2(av[i][2], av[i][3]);
-        o.z = pack_bf16x2(av[i][4], av[i][5]); o.w = pack_bf16x2(av[i][6], av[i][7]);
+        o.x = pack_bf16x2(av[0], av[1]); o.y = pack_bf16x2(av[2], av[3]);
+        o.z = pack_bf16x2(av[4], av[5]); o.w = pack_bf16x2(av[6], av[7]);
         *reinterpret_cast<uint4*>(y + size_t(t) * D + col) = o;
       }
     }
@@ -1073,8 +1074,8 @@ __global__ void __cluster_dims__(kBndCluster, 1, 1) __launch_bounds__(kBndThread
       const float inv = ue8m0_inv(sb);
       if (act && t < T) {
         uint2 wq;
-        wq.x = pack_fp8x4(av[i][0] * inv, av[i][1] * inv, av[i][2] * inv, av[i][3] * inv);
-        wq.y = pack_fp8x4(av[i][4] * inv, av[i][5] * inv, av[i][6] * inv, av[i][7] * inv);
+        wq.x = pack_fp8x4(av[0] * inv, av[1] * inv, av[2] * inv, av[3] * inv);
+        wq.y = pack_fp8x4(av[4] * inv, av[5] * inv, av[6] * inv, av[7] * inv);
         *reinterpret_cast<uint2*>(q + size_t(t) * D + col) = wq;
         if ((k & 15) == 0) reinterpret_cast<uint8_t*>(sf)[sf_byte_offset(t, col / 128, row_blocks)] = uint8_t(sb);
       }
@@ -1089,7 +1090,7 @@ cudaError_t mhc_boundary_small(void* X, int T, int D, const void* out, const flo
                                float* post_out, float* comb_out, cudaStream_t s) {
   if (T == 0) return cudaSuccess;
   const int Dc = D / kBndCluster;
-  if (D % (kBndCluster * 128) || Dc > kBndThreads * 8 || (out && (!post_in || !comb_in))) return cudaErrorInvalidValue;
+  if (D % (kBndCluster * 128) || Dc > kBndCols * 8 || (out && (!post_in || !comb_in))) return cudaErrorInvalidValue;
   constexpr int TT = 2;
   cb::launch_k(mhc_boundary_small_kernel<TT>, dim3(kBndCluster, ceil_div(T, TT)), kBndThreads, 0, s,
                reinterpret_cast<__nv_bfloat16*>(X), T, D, reinterpret_cast<const __nv_bfloat16*>(out), post_in,

@@ -1,6 +1,6 @@
 """Small, self-contained kernel cases for profiler captures (one launch of one kernel each, a few GB at most).
 
-    python -m carbon_b200.profile_cases gemm|grouped|moe_decode|attn|decode|decode_fp8|indexer|indexer_decode|ep_moe|oproj_a2a
+    python -m carbon_b200.profile_cases gemm|grouped|moe_decode|attn|decode|decode_fp8|boundary|indexer|indexer_decode|ep_moe|oproj_a2a
 
 Each case sets up inputs larger than L2 where it can, runs its kernel twice (warm-up + the launch to capture) and
 exits 0, so that ``ncu -k regex:<kernel> -s 1 -c 1`` captures exactly one warm launch.
@@ -92,6 +92,29 @@ def decode_fp8():
         sparse_mla(q, kv, idx, 192 ** -0.5, 512)
 
 
+def boundary():
+    """Fused decode mHC boundary at the full width: 32 tokens x 4 streams x 7168, post-mix + stats + coefficients +
+    pre-norm (two launches)."""
+    from .models.deepseek import make_hc
+    from .ops._ext import ext
+    from .ops.quant import empty_sf
+
+    T, D = 32, 7168
+    dev = torch.device("cuda")
+    hp = make_hc(torch.randn(24, 4 * D) * 0.02, torch.randn(24) * 0.5, torch.rand(3) + 0.5, dev)
+    w = torch.rand(D, device=dev) + 0.5
+    X = torch.randn(T, 4, D, device=dev).to(torch.bfloat16)
+    out = torch.randn(T, D, device=dev).to(torch.bfloat16)
+    post = torch.rand(T, 4, device=dev)
+    comb = torch.softmax(torch.randn(T, 4, 4, device=dev), -1)
+    y = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
+    q = torch.empty(T, D, dtype=torch.float8_e4m3fn, device=dev)
+    sf = empty_sf(T, D, dev)
+    p2, po2, c2 = torch.empty(T, 4, device=dev), torch.empty(T, 4, device=dev), torch.empty(T, 4, 4, device=dev)
+    for _ in range(2):
+        ext().mhc_boundary_small(X, out, post, comb, hp.fn, hp.base, hp.scale, 20, 1e-6, 1e-6, w, y, q, sf, p2, po2, c2)
+
+
 def indexer():
     from .ops.attention import indexer_prefill_mask
 
@@ -168,7 +191,7 @@ def oproj_a2a():
 
 if __name__ == "__main__":
     {"gemm": gemm, "grouped": grouped, "moe_decode": moe_decode, "attn": attn, "decode": decode,
-     "decode_fp8": decode_fp8,
+     "decode_fp8": decode_fp8, "boundary": boundary,
      "indexer": indexer, "indexer_decode": indexer_decode, "ep_moe": ep_moe, "oproj_a2a": oproj_a2a}[sys.argv[1]]()
     torch.cuda.synchronize()
     print("ok", sys.argv[1])

@@ -216,6 +216,16 @@ def latent_fp8_row_bytes(r: int, dr: int, mla: bool) -> int:
     return r + (na + 15) // 16 * 16 + (2 * dr if mla else 0)
 
 
+def _latent_fp8_offsets(r: int, dr: int, mla: bool):
+    """Byte layout of an fp8 row: [values of the first r/2 dims | scale bytes (padded to 16) | values of the last
+    r/2 dims | fp16 RoPE key (MLA)].  Each half of the decode kernel's CTA pair then reads one contiguous piece:
+    [0, r/2 + 16) and [r/2, end)."""
+    na = r // LATENT_ATOM
+    h = r // 2
+    sc = (na + 15) // 16 * 16
+    return h, h + sc, r + sc          # scales at h, second half of the values at h + sc, RoPE at r + sc
+
+
 def quant_latent_fp8(rows: torch.Tensor, r: int, dr: int, mla: bool) -> torch.Tensor:
     """[n, r (+ dr)] latent rows -> [n, row_bytes] uint8 in the fp8 cache format.  Each 64-dim atom gets the
     smallest power-of-two scale 2^e with amax / 2^e <= 448 (e clamped to [-126, 127]; 2^0 for an all-zero atom)
@@ -223,16 +233,20 @@ def quant_latent_fp8(rows: torch.Tensor, r: int, dr: int, mla: bool) -> torch.Te
     n = rows.shape[0]
     na = r // LATENT_ATOM
     rb = latent_fp8_row_bytes(r, dr, mla)
+    s_off, v2_off, pe_off = _latent_fp8_offsets(r, dr, mla)
+    h = r // 2
     x = rows[:, :r].float().reshape(n, na, LATENT_ATOM)
     amax = x.abs().amax(-1)
     m, ex = torch.frexp(amax / FP8_MAX)
     e = torch.where(amax > 0, ex - (m == 0.5).to(ex.dtype), torch.zeros_like(ex)).clamp(-126, 127)
     q = (x / torch.pow(2.0, e.float())[..., None]).clamp(-FP8_MAX, FP8_MAX).to(torch.float8_e4m3fn)
+    qb = q.reshape(n, r).view(torch.uint8)
     out = torch.zeros(n, rb, dtype=torch.uint8, device=rows.device)
-    out[:, :r] = q.reshape(n, r).view(torch.uint8)
-    out[:, r:r + na] = (e + 127).to(torch.uint8)
+    out[:, :h] = qb[:, :h]
+    out[:, s_off:s_off + na] = (e + 127).to(torch.uint8)
+    out[:, v2_off:v2_off + r - h] = qb[:, h:]
     if mla:
-        out[:, rb - 2 * dr:] = rows[:, r:r + dr].to(torch.float16).contiguous().view(torch.uint8)
+        out[:, pe_off:pe_off + 2 * dr] = rows[:, r:r + dr].to(torch.float16).contiguous().view(torch.uint8)
     return out
 
 
@@ -240,12 +254,14 @@ def dequant_latent_fp8(rows8: torch.Tensor, r: int, dr: int, mla: bool) -> torch
     """Inverse of ``quant_latent_fp8``: [n, row_bytes] uint8 -> [n, r (+ dr)] float32."""
     n = rows8.shape[0]
     na = r // LATENT_ATOM
-    rb = latent_fp8_row_bytes(r, dr, mla)
-    q = rows8[:, :r].contiguous().view(torch.float8_e4m3fn).float().reshape(n, na, LATENT_ATOM)
-    s = torch.pow(2.0, rows8[:, r:r + na].float() - 127.0)
+    s_off, v2_off, pe_off = _latent_fp8_offsets(r, dr, mla)
+    h = r // 2
+    qb = torch.cat([rows8[:, :h], rows8[:, v2_off:v2_off + r - h]], dim=1).contiguous()
+    q = qb.view(torch.float8_e4m3fn).float().reshape(n, na, LATENT_ATOM)
+    s = torch.pow(2.0, rows8[:, s_off:s_off + na].float() - 127.0)
     x = (q * s[..., None]).reshape(n, r)
     if mla:
-        x = torch.cat([x, rows8[:, rb - 2 * dr:].contiguous().view(torch.float16).float()], dim=1)
+        x = torch.cat([x, rows8[:, pe_off:pe_off + 2 * dr].contiguous().view(torch.float16).float()], dim=1)
     return x
 
 

@@ -16,8 +16,9 @@ def test_latent_fp8_format():
     q = R.quant_latent_fp8(x, 512, 64, True)
     assert q.shape == (6, 656) and R.latent_fp8_row_bytes(512, 64, True) == 656
     assert R.latent_fp8_row_bytes(512, 64, False) == 528
-    assert bool((q[:, 520:528] == 0).all())                    # scale padding
-    assert bool((q[0, 512:520] == 127).all())                  # all-zero atoms: scale 2^0
+    # layout: values of dims 0..255 | 8 scale bytes + 8 zero | values of dims 256..511 | fp16 RoPE key
+    assert bool((q[:, 264:272] == 0).all())                    # scale padding
+    assert bool((q[0, 256:264] == 127).all())                  # all-zero atoms: scale 2^0
     y = R.dequant_latent_fp8(q, 512, 64, True)
     assert torch.equal(y[:, 512:], x[:, 512:].half().float())  # RoPE key kept in fp16
     # per atom: |error| <= half an e4m3 step at the atom's scale (3 mantissa bits), relative to the atom's amax
@@ -26,7 +27,7 @@ def test_latent_fp8_format():
     big = amax[..., 0] > 1e-10
     assert bool(((ya - xa).abs() <= amax * 2.0 ** -4 + 1e-30)[big].all())
     # a scale byte is the smallest power of two that keeps the atom's amax within 448
-    e = q[:, 512:520].float() - 127
+    e = q[:, 256:264].float() - 127
     assert bool((amax[..., 0][big] <= 448 * torch.pow(2.0, e[big])).all())
     assert bool((amax[..., 0][big] > 224 * torch.pow(2.0, e[big])).all())
 
