@@ -121,8 +121,10 @@ def _owner_cfg(mode):
     if "v4" in mode:
         from carbon_b200.config import tiny_v4_config
 
-        return tiny_v4_config().replace(n_layers=3, index_sources=(1,), engram_layers=())
-    return tiny_config()
+        cfg = tiny_v4_config().replace(n_layers=3, index_sources=(1,), engram_layers=())
+    else:
+        cfg = tiny_config()
+    return cfg.replace(kv_fp8=True) if mode.endswith("_fp8kv") else cfg
 
 
 def _owner_worker(rank, world, port, q, mode="dp"):
@@ -178,7 +180,7 @@ def _owner_worker(rank, world, port, q, mode="dp"):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["dp", "tp", "tp_a2a", "tp_a2a_v4"])
+@pytest.mark.parametrize("mode", ["dp", "tp", "tp_a2a", "tp_a2a_v4", "tp_a2a_fp8kv"])
 def test_owner_kv_matches_single_rank_and_splits_pages(mode):
     """Owner-only KV on 2 ranks (DP attention, or TP attention whose cache-reading core runs token-parallel): each
     request's KV lives on its home rank only, yet the served tokens and logits equal the single-rank engine's, with
@@ -194,6 +196,18 @@ def test_owner_kv_matches_single_rank_and_splits_pages(mode):
     w = init_weights(cfg, seed=0)
     single = Engine(cfg, device="cpu", source=WeightSource(cfg, state=w), num_pages=48, page_size=16)
     ref_out, ref_hist = single.generate(_prompts(cfg), 5, return_logits=True)
+    ref_hist2 = []
+    if mode.endswith("_fp8kv"):
+        reqs = [single.add_request(p) for p in _prompts(cfg)]
+        logits = single.prefill_chunked(reqs, 24)
+        ref_hist2.append(logits)
+        nxt = torch.argmax(logits, -1).tolist()
+        for _ in range(4):
+            logits = single.decode(reqs, nxt)
+            ref_hist2.append(logits)
+            nxt = torch.argmax(logits, -1).tolist()
+        for r in reqs:
+            single.release(r)
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
     port = s.getsockname()[1]
@@ -213,7 +227,9 @@ def test_owner_kv_matches_single_rank_and_splits_pages(mode):
         assert spec == ref_out, (rank, spec, ref_out)
         for a, b in zip(hist, ref_hist):
             assert (torch.tensor(a) - b).abs().max() < 1e-3
-        for a, b in zip(hist2, ref_hist):                             # chunked prefill: the same logits
+        # chunked prefill: the same logits as the whole prompt (fp8 cache: as the single rank's chunked prefill, whose
+        # later chunks likewise attend over fp8-cached rows)
+        for a, b in zip(hist2, ref_hist2 if mode.endswith("_fp8kv") else ref_hist):
             assert (torch.tensor(a) - b).abs().max() < 1e-3
         assert sorted(set(homes)) == [0, 1]                         # both ranks own requests
         assert used == mine                                          # pages only for this rank's own requests

@@ -35,6 +35,8 @@ def _cfg(variant):
     from carbon_b200.config import tiny_v4_config
 
     variant = variant.replace("+a2a", "")
+    if variant.endswith("_fp8kv"):          # the same model over the fp8 latent KV cache
+        return _cfg(variant[: -len("_fp8kv")]).replace(kv_fp8=True)
     if variant == "sparse":                 # long-prompt MLA prefill as absorbed sparse attention
         return tiny_config().replace(sparse_prefill_min=40)
     if variant == "v4_late":
@@ -70,7 +72,8 @@ def _worker(rank, world, port, q, attn_dp=False, variant="v3"):
                                                    # TP attention with the head -> token all-to-all output projection
                                                    (2, False, "v3+a2a"), (4, False, "v3+a2a"), (2, False, "v4+a2a"),
                                                    (2, False, "v4_late+a2a"), (2, False, "skewed+a2a"),
-                                                   (2, False, "sparse"), (2, False, "sparse+a2a"), (2, True, "sparse")])
+                                                   (2, False, "sparse"), (2, False, "sparse+a2a"), (2, True, "sparse"),
+                                                   (2, False, "v3_fp8kv+a2a"), (2, True, "v4_fp8kv")])
 def test_tp_ep_engine_matches_single_rank(world, attn_dp, variant):
     cfg = _cfg(variant)
     w = init_weights(cfg, seed=0)
