@@ -160,10 +160,13 @@ def bench_decode_attn(a):
         ext().latent_store_fp8(kv, torch.arange(S, dtype=torch.int32, device="cuda"), kv8)
         kv, q, row = kv8, q.half(), 656
     idx = torch.stack([torch.randperm(a.context, device="cuda")[:K] + b * a.context for b in range(T)]).int()
+    if not a.unsorted:
+        idx = idx.sort(dim=1).values      # the DSA top-k hands keys over in key order (page order in the cache)
     ms = time_fn(lambda: sparse_mla(q, kv, idx, 192 ** -0.5, 512))
     bytes_kv = T * K * row
     pk = peaks()
-    print(json.dumps({"bench": "sparse_mla_decode", "kv": a.kv, "batch": T, "heads": H, "topk": K, "ms": round(ms, 4),
+    print(json.dumps({"bench": "sparse_mla_decode", "kv": a.kv, "key_order": "random" if a.unsorted else "sorted",
+                      "batch": T, "heads": H, "topk": K, "ms": round(ms, 4),
                       "kv_gbs": round(bytes_kv / ms / 1e6, 1),
                       "frac_of_hbm": round(bytes_kv / ms / 1e6 / pk["hbm_gbs"], 3),
                       "tflops": round(T * H * K * (576 + 512) * 2 / ms / 1e9, 1), "peak_src": pk["src"]}))
@@ -271,6 +274,8 @@ def main(argv=None):
     ap.add_argument("--heads", type=int, default=128)
     ap.add_argument("--dsa", action="store_true")
     ap.add_argument("--kv", default="bf16", choices=["bf16", "fp8"], help="decode_attn: latent cache format")
+    ap.add_argument("--unsorted", action="store_true",
+                    help="decode_attn: selected keys in random order (the engine passes them in key order)")
     ap.add_argument("--indexer-bf16", action="store_true", help="attn --dsa: bf16 indexer logits instead of fp8")
     ap.add_argument("--topk", type=int, default=2048, help="DSA top-k")
     ap.add_argument("--moe-topk", type=int, default=8, help="router top-k (moe)")

@@ -22,6 +22,22 @@
 namespace cb {
 namespace mla {
 
+// Timeline instrumentation for profiling builds (-DCB_DECODE_TRACE): the first CTA pair (token 0, split 0) records
+// the SM clock of each pipeline event of each tile into g_attn_trace[(cta * 8 + event) * 64 + tile].  Compiled out
+// otherwise.
+#ifdef CB_DECODE_TRACE
+__device__ long long* g_attn_trace;
+#define CB_ATTN_TRACE(ev, j)                                                                                     \
+  do {                                                                                                           \
+    if (g_attn_trace && blockIdx.x == 0 && blockIdx.z == 0 && (j) < 64)                                          \
+      g_attn_trace[(int(cluster_ctarank()) * 8 + (ev)) * 64 + (j)] = clock64();                                 \
+  } while (0)
+#else
+#define CB_ATTN_TRACE(ev, j) \
+  do {                       \
+  } while (0)
+#endif
+
 constexpr int HM = 128;                // head rows per CTA (M)
 // A row is NA 64-dim atoms: NA = 9 for MLA (512 latent + 64 RoPE key), NA = 8 for latent MQA (one 512-dim head whose
 // last 64 dims carry RoPE).  The value is always the first DL = 512 dims of the row.
@@ -146,7 +162,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
   uint64_t* x_full = pv_done + 2;            // [2]: the peer's partial of tile j landed in xbuf[j & 1] (tx bytes)
   uint64_t* x_empty = x_full + 2;            // [2]: the peer consumed this CTA's partial of tile j
   uint64_t* st_full = x_empty + 2;           // [F8_SLOTS] fp8: a slot's gathers landed (tx bytes)
-  uint64_t* st_empty = st_full + F8_SLOTS;   // [F8_SLOTS] fp8: both converter warps and Q·Kᵀ are done with a slot
+  uint64_t* st_empty = st_full + F8_SLOTS;   // [F8_SLOTS] fp8: both converter warps are done with a slot
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(st_empty + F8_SLOTS);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -205,6 +221,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok || *abort_flag) break;
+      if (lane == 0) CB_ATTN_TRACE(0, j);
       // lane (part, g): part = lane / 8, row group g = lane % 8 (rows 4g..4g+3)
       const int part = int(lane >> 3), g = int(lane & 7);
       const int r0 = __shfl_sync(0xffffffffu, slot, 4 * g), r1 = __shfl_sync(0xffffffffu, slot, 4 * g + 1);
@@ -274,6 +291,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
       fence_proxy_async();                   // generic-proxy stores -> visible to the tensor core's operand reads
       __syncwarp();
       if (lane == 0) { mbar_arrive(&kv_full[s]); mbar_arrive(&st_empty[s8]); }
+      if (lane == 0 && cw == 0) CB_ATTN_TRACE(1, j);
     }
   } else if (warp == 1) {
     // ---------------- MMA ----------------
@@ -294,6 +312,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
                        smem_desc_sw128(kb + kk * 32), id_qk, (la | kk) > 0);
         }
         mma_commit(&s_full[b]);
+        CB_ATTN_TRACE(2, j);
         return true;
       };
       auto issue_pv = [&](int j) -> bool {
@@ -307,6 +326,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
                      (j > 0 || k > 0) ? 1u : 0u);
         mma_commit(&pv_done[b]);
         mma_commit(&kv_empty[s]);
+        CB_ATTN_TRACE(3, j);
         return true;
       };
       if (ok) ok = issue_qk(0);
@@ -332,6 +352,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
       const int nk = k_begin + (j + 1) * KT + lane;
       next_slot = nk < k_end ? __ldg(idx_t + nk) : -1;
       if (!mbar_wait(&s_full[b], (j >> 1) & 1)) { fail(kErrTimeoutTmem); ok = false; break; }
+      if (row == 0) CB_ATTN_TRACE(4, j);
       tc_fence_after();
       uint32_t r[KT];
       tmem_ld_32x32b_x32(t_lane + TM_S + b * TM_S_STRIDE, r);
@@ -342,6 +363,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
       // my partial -> the peer's exchange buffer b (once the peer has consumed what I wrote there two tiles ago):
       // asynchronous stores whose bytes complete the peer's x_full[b], no fence on this side
       if (!mbar_wait(&x_empty[b], ((j >> 1) & 1) ^ 1)) { fail(kErrTimeoutPeer); ok = false; break; }
+      if (row == 0) CB_ATTN_TRACE(7, j);
       const uint32_t xrow = mapa_shared(smem_u32(xbuf + (b * HM + row) * X_LD), peer);
       const uint32_t xbar = mapa_shared(smem_u32(&x_full[b]), peer);
 #pragma unroll
@@ -349,6 +371,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
         st_async_v4(xrow + 16 * c, r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3], xbar);
       // the peer's partial of this tile
       if (!mbar_wait(&x_full[b], (j >> 1) & 1)) { fail(kErrTimeoutPeer); ok = false; break; }
+      if (row == 0) CB_ATTN_TRACE(5, j);
       const float4* xr = reinterpret_cast<const float4*>(xbuf + (b * HM + row) * X_LD);
       float sv[KT];
 #pragma unroll
@@ -401,6 +424,7 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[b]);
+      if (row == 0) CB_ATTN_TRACE(6, j);
     }
     if (ok && n_tiles > 0) {
       if (!mbar_wait(&pv_done[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1)) { fail(kErrTimeoutTmem); ok = false; }

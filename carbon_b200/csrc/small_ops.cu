@@ -28,10 +28,10 @@ __global__ void act_quant_kernel(const __nv_bfloat16* __restrict__ x, int ldx, u
                                  int x_rows) {
   cb::pdl_entry();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = blockIdx.y * 8 + warp;
   const int kg = blockIdx.x;
-  if (row >= M_pad) return;
-  if (n_blocks && row >= n_blocks[0] * 128) return;   // rows past the used 128-row blocks are never read
+  const int rows_used = n_blocks ? min(M_pad, n_blocks[0] * 128) : M_pad;   // rows past the used blocks: never read
+  // row groups stride over grid.y (at most 65535 groups of 8 rows per launch)
+  for (int row = blockIdx.y * 8 + warp; row < rows_used; row += gridDim.y * 8) {
   int src = row < M ? row : -1;
   if (src >= 0 && src_rows) src = src_rows[row];
   if (src >= x_rows) src = -1;                   // anything but a valid source row quantises as a zero row
@@ -80,13 +80,14 @@ __global__ void act_quant_kernel(const __nv_bfloat16* __restrict__ x, int ldx, u
     const int rb = row >> 7, r = row & 127;
     sf[(size_t(kg) * row_blocks + rb) * 128 + (r & 31) * 4 + (r >> 5)] = word;
   }
+  }
 }
 
 cudaError_t act_quant(const void* x, int ldx, void* q, int ldq, uint32_t* sf, int M, int K, const int* src_rows,
                       cudaStream_t s, const int* n_blocks, int x_rows) {
   if (x_rows < 0) x_rows = 0x7fffffff;
   const int row_blocks = ceil_div(M, 128), M_pad = row_blocks * 128;
-  dim3 grid(ceil_div(K, 512), ceil_div(M_pad, 8));
+  dim3 grid(ceil_div(K, 512), min(ceil_div(M_pad, 8), 65535));
   cb::launch_k(act_quant_kernel, grid, 256, 0, s, reinterpret_cast<const __nv_bfloat16*>(x), ldx,
                                         reinterpret_cast<uint8_t*>(q), ldq, sf, M, K, row_blocks, src_rows, M_pad,
                                         n_blocks, x_rows);
@@ -1173,3 +1174,4 @@ cudaError_t silu_mul(const void* gu, int T, int I, float limit, void* out, cudaS
 }
 
 }  // namespace cb
+

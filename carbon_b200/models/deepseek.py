@@ -802,8 +802,9 @@ class DeepseekModel:
             else:
                 idx = self._dsa[src]                # selection shared with the index-source layer
         with region("attn.absorb_q"):
-            q_abs = head_bmm(q[..., :dn], L.w_uk)                                    # [T, Hl, r]
-            qf = torch.cat([q_abs.to(self.act_dtype), q[..., dn:].to(self.act_dtype)], dim=-1).contiguous()
+            # [q_nope · W_uk | q_rope] -> [T, Hl, r + dr], in fp16 when the kernel reads fp8 cache rows
+            qf = head_bmm(q, L.w_uk, tail=q.shape[-1] - dn,
+                          out_dtype=torch.float16 if (self.on_gpu and cfg.kv_fp8) else self.act_dtype).contiguous()
         if pending is not None:
             idx = pending.get()
             self._dsa[i] = idx
@@ -1056,12 +1057,17 @@ def mhc_mix(x: torch.Tensor, fn: torch.Tensor) -> torch.Tensor:
     return bf16_gemm(x, fn, out_dtype=torch.float32)
 
 
-def head_bmm(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
-    """Per-head matmul: x [T, H, K] · w[h]ᵀ (w [H, N, K]) -> [T, H, N]."""
-    T, H, K = x.shape
-    N = w.shape[1]
+def head_bmm(x: torch.Tensor, w: torch.Tensor, tail: int = 0, out_dtype=torch.bfloat16) -> torch.Tensor:
+    """Per-head matmul: x [T, H, K(+tail)] · w[h]ᵀ (w [H, N, K]) -> [T, H, N(+tail)]; with ``tail`` the last
+    columns of x are appended unchanged (the absorbed query [q_nope · W_uk | q_rope]) in ``out_dtype``."""
+    T, H, Kx = x.shape
+    N, K = w.shape[1], w.shape[2]
     if not x.is_cuda:
-        return torch.einsum("thk,hnk->thn", x.float(), w.float())
+        out = torch.einsum("thk,hnk->thn", x[..., :K].float(), w.float())
+        return torch.cat([out, x[..., K:K + tail].float()], dim=-1) if tail else out
+    if tail:
+        return torch.cat([head_bmm(x[..., :K], w).to(out_dtype), x[..., K:K + tail].to(out_dtype)], dim=-1)
+    x = x[..., :K]
     Tp = ((T + 127) // 128) * 128
     # head-major rows, each head's block padded to 128 rows; the padding rows are never read back (every output
     # row depends only on its own input row), so they stay uninitialised

@@ -72,7 +72,7 @@ def decode():
     T, K, S = 32, 2048, 32 * 4096
     q = torch.randn(T, 128, 576, device="cuda").to(torch.bfloat16)
     kv = torch.randn(S, 576, device="cuda").to(torch.bfloat16)
-    idx = torch.stack([torch.randperm(4096, device="cuda")[:K] + b * 4096 for b in range(T)]).int()
+    idx = torch.stack([torch.randperm(4096, device="cuda")[:K] + b * 4096 for b in range(T)]).int().sort(1).values
     for _ in range(2):
         sparse_mla(q, kv, idx, 192 ** -0.5, 512)
 
@@ -87,7 +87,7 @@ def decode_fp8():
     rows = torch.randn(S, 576, device="cuda").to(torch.bfloat16)
     kv = torch.empty(S, 656, dtype=torch.uint8, device="cuda")
     ext().latent_store_fp8(rows, torch.arange(S, dtype=torch.int32, device="cuda"), kv)
-    idx = torch.stack([torch.randperm(4096, device="cuda")[:K] + b * 4096 for b in range(T)]).int()
+    idx = torch.stack([torch.randperm(4096, device="cuda")[:K] + b * 4096 for b in range(T)]).int().sort(1).values
     for _ in range(2):
         sparse_mla(q, kv, idx, 192 ** -0.5, 512)
 

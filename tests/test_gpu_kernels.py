@@ -507,3 +507,4 @@ def test_mhc_boundary_fused_matches_separate_kernels(T, with_out, D):
     da = qa.float().cpu() * unpack_sf(sfa.cpu(), T, D).repeat_interleave(128, 1)
     db = qb.float().cpu() * unpack_sf(sfb.cpu(), T, D).repeat_interleave(128, 1)
     assert rel_err(db, da) < 2e-2, rel_err(db, da)
+
