@@ -46,6 +46,9 @@ def parse():
     ap.add_argument("--layers", type=int, default=0, help="override layer count (0 = config's)")
     ap.add_argument("--mem-frac", type=float, default=0.62, help="HBM fraction for weights (rest: cache, acts)")
     ap.add_argument("--profile", action="store_true", help="print per-region device times (stderr)")
+    ap.add_argument("--kernel-table", action="store_true",
+                    help="print the device time per kernel of one graph-replayed decode step (CUPTI activity records "
+                         "through torch.profiler; for analysis, never a bench value)")
     ap.add_argument("--trace-dir", default=None,
                     help="with --profile: write Chrome trace files of the traced decode and prefill steps here "
                          "(one per rank)")
@@ -304,6 +307,23 @@ def main():
     tpot_p50 = max_over_ranks(statistics.median(tp), world)
 
     tables = []
+    if args.kernel_table:                  # every rank replays the same step (it contains collectives)
+        from torch.profiler import ProfilerActivity, profile
+
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            eng.decode(reqs, next_ids())
+            torch.cuda.synchronize()
+        agg = {}
+        for ev in prof.events():
+            if ev.device_type.name == "CUDA":
+                k = ev.name.split("(")[0][:70]
+                n, us = agg.get(k, (0, 0.0))
+                agg[k] = (n + 1, us + ev.device_time)
+        total = sum(us for _, us in agg.values())
+        rows = sorted(agg.items(), key=lambda kv: -kv[1][1])
+        tables.append("== decode step, device time per kernel (graph replay) ==\n" + "\n".join(
+            f"{us:10.1f} us {n:5d}  {100 * us / max(total, 1e-9):5.1f}%  {k}" for k, (n, us) in rows[:40]) +
+            f"\n{total:10.1f} us total")
     if args.profile:                       # every rank runs the traced steps (they contain collectives)
         from carbon_b200.utils.trace import tracing
 
@@ -324,8 +344,8 @@ def main():
         tables.append("== prefill regions ==\n" + t.table())
         if args.trace_dir:
             t.chrome_trace(os.path.join(args.trace_dir, f"prefill_rank{rank}.json"), pid=rank)
-        if rank == 0:
-            print("\n".join(tables), file=sys.stderr, flush=True)
+    if tables and rank == 0:
+        print("\n".join(tables), file=sys.stderr, flush=True)
     if world > 1:
         dist.barrier()
     if rank == 0:

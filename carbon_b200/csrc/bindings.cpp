@@ -192,6 +192,22 @@ void mhc_boundary_small(torch::Tensor X, c10::optional<torch::Tensor> out, c10::
   if (q.has_value()) CK(cb::sf_pad(reinterpret_cast<uint32_t*>(sf->data_ptr()), T, D, cur_stream()));
 }
 
+// DSA indexer key / head-weight post-processing (LayerNorm + RoPE of the key, scaled head weights) in one launch
+void indexer_kw_post(torch::Tensor kw, int64_t Di, torch::Tensor ln_w, torch::Tensor ln_b, double eps,
+                     torch::Tensor cos_sin, torch::Tensor pos, int64_t dr, double wscale, torch::Tensor k,
+                     torch::Tensor w) {
+  CHECK_CUDA(kw); CHECK_DT(kw, at::kFloat); CHECK_DT(ln_w, at::kFloat); CHECK_DT(ln_b, at::kFloat);
+  CHECK_DT(cos_sin, at::kFloat); CHECK_DT(pos, at::kInt); CHECK_DT(k, at::kBFloat16); CHECK_DT(w, at::kFloat);
+  CHECK_CONTIG(k); CHECK_CONTIG(w); CHECK_CONTIG(pos); CHECK_CONTIG(cos_sin);
+  TORCH_CHECK(kw.dim() == 2 && kw.stride(1) == 1, "indexer_kw_post: kw [T, Di + Hi]");
+  const int T = kw.size(0), Hi = kw.size(1) - int(Di);
+  TORCH_CHECK(k.numel() == int64_t(T) * Di && w.numel() == int64_t(T) * Hi && pos.numel() >= T, "shapes");
+  c10::cuda::CUDAGuard g(kw.device());
+  CK(cb::indexer_kw_post(kw.data_ptr<float>(), kw.stride(0), T, int(Di), Hi, ln_w.data_ptr<float>(),
+                         ln_b.data_ptr<float>(), float(eps), cos_sin.data_ptr<float>(), pos.data_ptr<int>(), int(dr),
+                         float(wscale), k.data_ptr(), w.data_ptr<float>(), cur_stream()));
+}
+
 void embed_hc(torch::Tensor table, int64_t row_lo, torch::Tensor ids, torch::Tensor X,
               c10::optional<torch::Tensor> sumsq) {
   CHECK_CUDA(table); CHECK_DT(table, at::kBFloat16); CHECK_CONTIG(table); CHECK_DT(ids, at::kInt);
@@ -482,6 +498,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mhc_head_coeffs", &mhc_head_coeffs);
   m.def("mhc_pre_norm", &mhc_pre_norm);
   m.def("mhc_boundary_small", &mhc_boundary_small);
+  m.def("indexer_kw_post", &indexer_kw_post);
   m.def("mhc_post_mix", &mhc_post_mix);
   m.def("embed_hc", &embed_hc);
   m.def("row_sumsq", &row_sumsq);

@@ -146,49 +146,72 @@ __global__ void splitk_reduce_out_kernel(const float* __restrict__ part, int spl
 }
 
 // Split-K partials of an interleaved gate/up GEMM (N = 2I, 128-column chunks gate|up) -> SwiGLU -> fp8 + SF tiles,
-// exactly the SwiGLU epilogue's arithmetic.  One warp per (row, 128 output columns), 4 outputs per lane; warps
-// stride over the work (a grouped call's row count is only known on the device: n_blocks * 128 rows, so the grid is
-// sized for the SMs, not for the padded capacity).
+// exactly the SwiGLU epilogue's arithmetic.  One warp per (row, 128 output columns), 4 outputs per lane.
+CB_DEVICE void swiglu_reduce_row(const float* __restrict__ part, int splits, int M, int N, float limit,
+                                 uint8_t* __restrict__ out, int ldo, uint32_t* __restrict__ out_sf, int sf_row_blocks,
+                                 int row, int g, int lane) {
+  float a[4];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int t = 4 * lane + i;
+    float gv = 0.f, uv = 0.f;
+    for (int sp = 0; sp < splits; ++sp) {
+      const float* pr = part + (size_t(sp) * M + row) * N + 256 * g;
+      gv += pr[t];
+      uv += pr[128 + t];
+    }
+    if (limit > 0.f) { gv = fminf(gv, limit); uv = fminf(fmaxf(uv, -limit), limit); }
+    a[i] = gv / (1.f + __expf(-gv)) * uv;
+    amax = fmaxf(amax, fabsf(a[i]));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+  const uint32_t sb = ue8m0_for_amax(amax);
+  const float inv = ue8m0_inv(sb);
+  *reinterpret_cast<uint32_t*>(out + size_t(row) * ldo + 128 * g + 4 * lane) =
+      pack_fp8x4(a[0] * inv, a[1] * inv, a[2] * inv, a[3] * inv);
+  if (lane == 0) {
+    const int rb = row / 128, r = row % 128;
+    uint8_t* sf = reinterpret_cast<uint8_t*>(out_sf) +
+                  ((size_t(g >> 2) * sf_row_blocks + rb) * 128 + (r % 32) * 4 + (r / 32)) * 4 + (g & 3);
+    *sf = uint8_t(sb);
+  }
+}
+
+// Dense calls (row_valid == nullptr): warps stride over every (row, column group).  Grouped calls (a row_valid map,
+// the used 128-row blocks counted on the device): one CTA per 128-row block; CTAs past the used blocks and padding
+// rows return at once, so a decode call touches only its few routed rows out of the padded capacity.
 __global__ void splitk_reduce_swiglu_kernel(const float* __restrict__ part, int splits, int M, int N, float limit,
                                             uint8_t* __restrict__ out, int ldo, uint32_t* __restrict__ out_sf,
                                             int sf_row_blocks, const int* __restrict__ row_valid,
                                             const int* __restrict__ n_blocks) {
   cb::pdl_entry();
-  const int I = N / 2, chunks = I / 128;
-  const int lane = threadIdx.x & 31;
-  const int rows = n_blocks ? min(M, n_blocks[0] * 128) : M;
-  const int nw = gridDim.x * (blockDim.x >> 5);
-  for (int wg = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); wg < rows * chunks; wg += nw) {
-    const int row = wg / chunks, g = wg % chunks;
-    if (row_valid && row_valid[row] < 0) continue;  // padding rows of an expert segment: never read back
-    float a[4];
-    float amax = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int t = 4 * lane + i;
-      float gv = 0.f, uv = 0.f;
-      for (int sp = 0; sp < splits; ++sp) {
-        const float* pr = part + (size_t(sp) * M + row) * N + 256 * g;
-        gv += pr[t];
-        uv += pr[128 + t];
-      }
-      if (limit > 0.f) { gv = fminf(gv, limit); uv = fminf(fmaxf(uv, -limit), limit); }
-      a[i] = gv / (1.f + __expf(-gv)) * uv;
-      amax = fmaxf(amax, fabsf(a[i]));
+  const int chunks = N / 256;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  if (row_valid) {
+    if (n_blocks && int(blockIdx.x) >= n_blocks[0]) return;
+    // the block's rows that carry a token (padding rows of an expert segment are never read back), then every
+    // (row, column group) pair of them spread over the warps
+    __shared__ int rows_s[128];
+    __shared__ int n_s;
+    if (threadIdx.x == 0) n_s = 0;
+    __syncthreads();
+    for (int rr = threadIdx.x; rr < 128; rr += blockDim.x) {
+      const int row = blockIdx.x * 128 + rr;
+      if (row < M && row_valid[row] >= 0) rows_s[atomicAdd(&n_s, 1)] = row;
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const uint32_t sb = ue8m0_for_amax(amax);
-    const float inv = ue8m0_inv(sb);
-    *reinterpret_cast<uint32_t*>(out + size_t(row) * ldo + 128 * g + 4 * lane) =
-        pack_fp8x4(a[0] * inv, a[1] * inv, a[2] * inv, a[3] * inv);
-    if (lane == 0) {
-      const int rb = row / 128, r = row % 128;
-      uint8_t* sf = reinterpret_cast<uint8_t*>(out_sf) +
-                    ((size_t(g >> 2) * sf_row_blocks + rb) * 128 + (r % 32) * 4 + (r / 32)) * 4 + (g & 3);
-      *sf = uint8_t(sb);
-    }
+    __syncthreads();
+    const int n = n_s;
+    for (int item = warp; item < n * chunks; item += nwarps)
+      swiglu_reduce_row(part, splits, M, N, limit, out, ldo, out_sf, sf_row_blocks, rows_s[item / chunks],
+                        item % chunks, lane);
+    return;
   }
+  const int rows = n_blocks ? min(M, n_blocks[0] * 128) : M;
+  const int nw = gridDim.x * nwarps;
+  for (int wg = blockIdx.x * nwarps + warp; wg < rows * chunks; wg += nw)
+    swiglu_reduce_row(part, splits, M, N, limit, out, ldo, out_sf, sf_row_blocks, wg / chunks, wg % chunks, lane);
 }
 
 // K splits for a dense fp8 GEMM whose output tiles cannot occupy the SMs (decode-sized M): whole 512-wide scale
@@ -279,9 +302,9 @@ cudaError_t gemm_fp8(const void* A, const void* B, const uint32_t* sfa, const ui
       p.out = work; p.ldo = N;
       cudaError_t e = launch<KIND_MXF8, EPI_F32, 128, 6, 2>(ta, tb, p, max_tiles, num_sms, s);
       if (e != cudaSuccess) return e;
-      const int warps = M * (N / 256);
-      cb::launch_k(splitk_reduce_swiglu_kernel, min(ceil_div(warps, 8), num_sms * 8), 256, 0, s, work, 1, M, N,
-                   swiglu_limit,
+      // one CTA per 128-row block when a row map is given (grouped call), else warps striding over the rows
+      const int grid = row_valid ? ceil_div(M, 128) : min(ceil_div(M * (N / 256), 8), num_sms * 8);
+      cb::launch_k(splitk_reduce_swiglu_kernel, grid, 256, 0, s, work, 1, M, N, swiglu_limit,
                                                                      reinterpret_cast<uint8_t*>(out), ldo, out_sf,
                                                                      ceil_div(M, 128), row_valid, num_m_blocks_dev);
       return cudaGetLastError();

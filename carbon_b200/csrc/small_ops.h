@@ -35,6 +35,11 @@ cudaError_t mhc_head_coeffs(const float* mix, int ld_mix, const float* sumsq, co
                             int T, int flat_dim, float hc_eps, float rms_eps, float* pre, cudaStream_t s);
 cudaError_t mhc_pre_norm(const void* X, const float* pre, const float* w, int T, int D, float eps, void* y, void* q,
                          uint32_t* sf, const int* rows, cudaStream_t s);
+// DSA indexer post-processing of the fused [wk | weights_proj] fp32 projection kw [T, ld >= Di + Hi]: k [T, Di] bf16
+// = RoPE(LayerNorm(kw[:, :Di])) (RoPE on dims [0, dr)), w [T, Hi] fp32 = kw[:, Di:] * wscale
+cudaError_t indexer_kw_post(const float* kw, int ld, int T, int Di, int Hi, const float* ln_w, const float* ln_b,
+                            float eps, const float* cos_sin, const int* pos, int dr, float wscale, void* k, float* w,
+                            cudaStream_t s);
 // Fused decode-size mHC boundary (post-mix of `out` when given, the next sublayer's statistics and coefficients,
 // pre-mix + RMSNorm + bf16 / fp8 outputs); X [T, 4, D] bf16 updated in place; D a multiple of 1024, at most 8192
 cudaError_t mhc_boundary_small(void* X, int T, int D, const void* out, const float* post_in, const float* comb_in,

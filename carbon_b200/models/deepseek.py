@@ -592,14 +592,21 @@ class DeepseekModel:
             q = q.clone()
         C.rope_(q, 0, dr, self.cos_sin, pos)
         if self.on_gpu:
+            from ..ops._ext import ext
+
             kw = L.idx_wkp(h, out_dtype=torch.float32)                               # [T, Di + Hi]
-            k = F.layer_norm(kw[:, :Di], (Di,), L.idx_kn_w, L.idx_kn_b, 1e-6).to(self.act_dtype)
-            w = kw[:, Di:] * ((Hi ** -0.5) * (Di ** -0.5))
+            k = torch.empty(T, Di, dtype=torch.bfloat16, device=h.device)
+            w = torch.empty(T, Hi, dtype=torch.float32, device=h.device)
+            # LayerNorm + RoPE of the key and the scaled head weights in one launch
+            ext().indexer_kw_post(kw, Di, L.idx_kn_w.float().contiguous(), L.idx_kn_b.float().contiguous(), 1e-6,
+                                  self.cos_sin, pos.to(torch.int32).contiguous(), dr, (Hi ** -0.5) * (Di ** -0.5),
+                                  k, w)
+            k = k.view(T, 1, Di)
         else:
             k = F.layer_norm(L.idx_wk(h).float(), (Di,), L.idx_kn_w, L.idx_kn_b, 1e-6).to(self.act_dtype)
             w = (L.idx_wp(h, out_dtype=torch.float32) * (Hi ** -0.5) * (Di ** -0.5)).float()
-        k = k.view(T, 1, Di)
-        C.rope_(k, 0, dr, self.cos_sin, pos)
+            k = k.view(T, 1, Di)
+            C.rope_(k, 0, dr, self.cos_sin, pos)
         if cfg.index_fp4:               # fp4 values are exact in bf16: the bf16 logits kernels compute fp4 products
             q = R.fake_quant_mxfp4(q)
             k = R.fake_quant_mxfp4(k)

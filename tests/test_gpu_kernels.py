@@ -508,3 +508,26 @@ def test_mhc_boundary_fused_matches_separate_kernels(T, with_out, D):
     db = qb.float().cpu() * unpack_sf(sfb.cpu(), T, D).repeat_interleave(128, 1)
     assert rel_err(db, da) < 2e-2, rel_err(db, da)
 
+
+
+@pytest.mark.parametrize("T", [1, 32, 300])
+def test_indexer_kw_post_vs_torch(T):
+    """Indexer key LayerNorm + RoPE and scaled head weights in one kernel, against the separate torch / RoPE ops."""
+    import torch.nn.functional as F
+
+    from carbon_b200.ops import core as C
+
+    torch.manual_seed(41)
+    Di, Hi, dr = 128, 64, 64
+    kw = (torch.randn(T, Di + Hi) * 3).to(DEV)
+    lw, lb = (torch.rand(Di) + 0.5).to(DEV), (torch.randn(Di) * 0.1).to(DEV)
+    table = C.rope_table(4096, dr, 10000.0, DEV)
+    pos = torch.randint(0, 4096, (T,), dtype=torch.int32, device=DEV)
+    k = torch.empty(T, Di, dtype=torch.bfloat16, device=DEV)
+    w = torch.empty(T, Hi, device=DEV)
+    _ext().indexer_kw_post(kw, Di, lw, lb, 1e-6, table, pos, dr, 0.01, k, w)
+    ref_k = F.layer_norm(kw[:, :Di], (Di,), lw, lb, 1e-6).to(torch.bfloat16).view(T, 1, Di)
+    C.rope_(ref_k, 0, dr, table, pos)
+    torch.cuda.synchronize()
+    assert torch.allclose(w, kw[:, Di:] * 0.01)
+    assert rel_err(k, ref_k.view(T, Di)) < 5e-3, rel_err(k, ref_k.view(T, Di))
