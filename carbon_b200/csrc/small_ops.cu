@@ -94,8 +94,8 @@ cudaError_t act_quant(const void* x, int ldx, void* q, int ldq, uint32_t* sf, in
   return cudaGetLastError();
 }
 
-// Gather of already-quantised rows: dst row r = src row src_rows[r] (fp8 bytes and its SF words; -1 = zero row with
-// unit scales).  One warp per destination row; rows past n_blocks*128 are left alone.  Used by the MoE dispatch so
+// Gather of already-quantised rows: dst row r = src row src_rows[r] (fp8 bytes and its SF words; -1 = a padding row,
+// not written).  One warp per destination row; rows past n_blocks*128 are left alone.  Used by the MoE dispatch so
 // that every token is quantised once instead of once per selected expert.
 __global__ void gather_fp8_rows_kernel(const uint8_t* __restrict__ src, const uint32_t* __restrict__ src_sf,
                                        int src_rows_n, int K, const int* __restrict__ src_rows, int M,
@@ -108,14 +108,16 @@ __global__ void gather_fp8_rows_kernel(const uint8_t* __restrict__ src, const ui
   if (n_blocks && row >= n_blocks[0] * 128) return;
   int sr = src_rows[row];
   if (sr >= 0 && !cb_check_index(sr, src_rows_n, "gather_fp8_rows")) sr = -1;
-  const uint4* s4 = reinterpret_cast<const uint4*>(src + size_t(sr < 0 ? 0 : sr) * K);
+  // padding rows of an expert segment are left as they are: every output row of the grouped GEMMs depends on its
+  // own input row only, and no consumer reads a padding row's output (writing zeros cost ~150 MB per decode call)
+  if (sr < 0) return;
+  const uint4* s4 = reinterpret_cast<const uint4*>(src + size_t(sr) * K);
   uint4* d4 = reinterpret_cast<uint4*>(dst + size_t(row) * K);
-  for (int c = lane; c < K / 16; c += 32) d4[c] = sr < 0 ? make_uint4(0, 0, 0, 0) : s4[c];
+  for (int c = lane; c < K / 16; c += 32) d4[c] = s4[c];
   const int kgroups = (K + 511) / 512;
   const int src_rb = (src_rows_n + 127) / 128, dst_rb = (M + 127) / 128;
   for (int kg = lane; kg < kgroups; kg += 32) {
-    uint32_t w = 0x7f7f7f7fu;                       // unit scales for a zero row
-    if (sr >= 0) w = src_sf[(size_t(kg) * src_rb + (sr >> 7)) * 128 + (sr & 31) * 4 + ((sr & 127) >> 5)];
+    const uint32_t w = src_sf[(size_t(kg) * src_rb + (sr >> 7)) * 128 + (sr & 31) * 4 + ((sr & 127) >> 5)];
     dst_sf[(size_t(kg) * dst_rb + (row >> 7)) * 128 + (row & 31) * 4 + ((row & 127) >> 5)] = w;
   }
 }
@@ -443,16 +445,24 @@ __global__ void moe_offsets_kernel(const int* __restrict__ cnt, int E, int align
   const int incl = v + (wid > 0 ? wsum[wid - 1] : 0);
   const int st = incl - padded;
   const int max_rows = max_blocks * 128;
+  __shared__ int st_s[1024], c_s[1024];
   if (t < E) {
     start[t] = st;
     fill[t] = 0;
+    st_s[t] = st;
+    c_s[t] = c;
     for (int b = st >> 7; b < (st + padded) >> 7 && b < max_blocks; ++b) m_block_expert[b] = t;
-    for (int r = st + c; r < st + padded && r < max_rows; ++r) row_src[r] = -1;   // padding rows
   }
   const int total_blocks = s_total >> 7;
   if (t == 0) num_blocks[0] = total_blocks;
   for (int b = total_blocks + t; b < max_blocks; b += blockDim.x) m_block_expert[b] = -1;
-  for (int r = s_total + t; r < max_rows; r += blockDim.x) row_src[r] = -1;   // rows past the used blocks
+  __syncthreads();                              // the block -> expert map above is visible to the whole CTA
+  // padding rows of each expert segment and every row past the used blocks -> -1, all threads over all rows
+  for (int r = t; r < max_rows; r += blockDim.x) {
+    const int b = r >> 7;
+    const int e = b < total_blocks ? m_block_expert[b] : -1;
+    if (e < 0 || r - st_s[e] >= c_s[e]) row_src[r] = -1;
+  }
 }
 
 __global__ void moe_scatter_kernel(const int* __restrict__ ids, int Tk, int k, int E, const int* __restrict__ start,
@@ -914,6 +924,12 @@ __global__ void __cluster_dims__(kBndCluster, 1, 1) __launch_bounds__(kBndThread
     }
   }
   // ---- B: statistics partials over this CTA's columns of stream g, 8 fn rows at a time ----
+  uint4 fnext[8];                                            // fn rows of the next group, loaded a group ahead
+  if (act) {
+#pragma unroll
+    for (int rr = 0; rr < 8; ++rr)
+      fnext[rr] = __ldg(reinterpret_cast<const uint4*>(fn + size_t(rr) * FD + size_t(g) * D + col));
+  }
   for (int r0 = 0; r0 < kBndStats; r0 += 8) {
     float acc[TT][8];
 #pragma unroll
@@ -923,8 +939,12 @@ __global__ void __cluster_dims__(kBndCluster, 1, 1) __launch_bounds__(kBndThread
     if (act) {
       uint4 fv[8];
 #pragma unroll
-      for (int rr = 0; rr < 8; ++rr)
-        fv[rr] = __ldg(reinterpret_cast<const uint4*>(fn + size_t(r0 + rr) * FD + size_t(g) * D + col));
+      for (int rr = 0; rr < 8; ++rr) fv[rr] = fnext[rr];
+      if (r0 + 8 < kBndStats) {
+#pragma unroll
+        for (int rr = 0; rr < 8; ++rr)
+          fnext[rr] = __ldg(reinterpret_cast<const uint4*>(fn + size_t(r0 + 8 + rr) * FD + size_t(g) * D + col));
+      }
 #pragma unroll
       for (int rr = 0; rr < 8; ++rr) {
         const float f[8] = {bf16_lo(fv[rr].x), bf16_hi(fv[rr].x), bf16_lo(fv[rr].y), bf16_hi(fv[rr].y),
@@ -966,13 +986,13 @@ __global__ void __cluster_dims__(kBndCluster, 1, 1) __launch_bounds__(kBndThread
   cluster_sync();                                            // every CTA's partials are visible cluster-wide
   for (int e = threadIdx.x; e < TT * (kBndStats + 1); e += kBndThreads) {
     const uint32_t a = smem_u32(&red[0][0] + e);
+    float x[kBndCluster];
+#pragma unroll
+    for (int cc = 0; cc < kBndCluster; ++cc)   // every load in flight before the first add
+      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x[cc]) : "r"(mapa_shared(a, uint32_t(cc))));
     float v = 0.f;
 #pragma unroll
-    for (int cc = 0; cc < kBndCluster; ++cc) {
-      float x;
-      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x) : "r"(mapa_shared(a, uint32_t(cc))));
-      v += x;
-    }
+    for (int cc = 0; cc < kBndCluster; ++cc) v += x[cc];
     (&tot[0][0])[e] = v;
   }
   __syncthreads();
@@ -996,14 +1016,14 @@ __global__ void __cluster_dims__(kBndCluster, 1, 1) __launch_bounds__(kBndThread
     cv = cv / s + hc_eps;
     s = cv + __shfl_xor_sync(0xffffffffu, cv, 4);             // column sums
     s += __shfl_xor_sync(0xffffffffu, s, 8);
-    cv /= (s + hc_eps);
-    for (int it = 1; it < iters; ++it) {
+    cv = __fdividef(cv, s + hc_eps);
+    for (int it = 1; it < iters; ++it) {                      // approximate divisions (2 ulp): latency-bound loop
       s = cv + __shfl_xor_sync(0xffffffffu, cv, 1);
       s += __shfl_xor_sync(0xffffffffu, s, 2);
-      cv /= (s + hc_eps);
+      cv = __fdividef(cv, s + hc_eps);
       s = cv + __shfl_xor_sync(0xffffffffu, cv, 4);
       s += __shfl_xor_sync(0xffffffffu, s, 8);
-      cv /= (s + hc_eps);
+      cv = __fdividef(cv, s + hc_eps);
     }
     if (lane < 16) coef[i][8 + lane] = cv;
     __syncwarp();
@@ -1042,13 +1062,13 @@ __global__ void __cluster_dims__(kBndCluster, 1, 1) __launch_bounds__(kBndThread
   cluster_sync();
   if (threadIdx.x < TT) {
     const uint32_t a = smem_u32(&red2[threadIdx.x]);
+    float x[kBndCluster];
+#pragma unroll
+    for (int cc = 0; cc < kBndCluster; ++cc)
+      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x[cc]) : "r"(mapa_shared(a, uint32_t(cc))));
     float v = 0.f;
 #pragma unroll
-    for (int cc = 0; cc < kBndCluster; ++cc) {
-      float x;
-      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x) : "r"(mapa_shared(a, uint32_t(cc))));
-      v += x;
-    }
+    for (int cc = 0; cc < kBndCluster; ++cc) v += x[cc];
     nrm[threadIdx.x] = rsqrtf(v / float(D) + rms_eps);
   }
   __syncthreads();
@@ -1175,3 +1195,43 @@ cudaError_t silu_mul(const void* gu, int T, int I, float limit, void* out, cudaS
 
 }  // namespace cb
 
+
+namespace cb {
+
+// DSA indexer key / weight post-processing of the fused [wk | weights_proj] projection, one launch per call:
+// k[t] = RoPE(bf16(LayerNorm(kw[t, :Di]) * ln_w + ln_b)) on dims [0, dr) (interleaved pairs, the bf16 values rotated
+// in fp32 and rounded again), w[t, h] = kw[t, Di + h] * wscale.  One CTA of Di threads per token (Di <= 1024, even).
+__global__ void indexer_kw_post_kernel(const float* __restrict__ kw, int ld, int Di, int Hi,
+                                       const float* __restrict__ ln_w, const float* __restrict__ ln_b, float eps,
+                                       const float* __restrict__ cos_sin, const int* __restrict__ pos, int dr,
+                                       float wscale, __nv_bfloat16* __restrict__ k, float* __restrict__ w) {
+  cb::pdl_entry();
+  __shared__ float red[32];
+  const int t = blockIdx.x, d = threadIdx.x;
+  const float* row = kw + size_t(t) * ld;
+  const float x = row[d];
+  const float mean = block_sum(x, red) / float(Di);
+  const float dx = x - mean;
+  const float var = block_sum(dx * dx, red) / float(Di);
+  float y = __bfloat162float(__float2bfloat16_rn(dx * rsqrtf(var + eps) * ln_w[d] + ln_b[d]));
+  const float other = __shfl_xor_sync(0xffffffffu, y, 1);    // the pair partner (pairs never straddle a warp)
+  if (d < dr) {
+    const int p = pos[t];
+    const float c = cos_sin[size_t(p) * dr + (d & ~1)], s = cos_sin[size_t(p) * dr + (d & ~1) + 1];
+    y = (d & 1) ? other * s + y * c : y * c - other * s;
+  }
+  k[size_t(t) * Di + d] = __float2bfloat16_rn(y);
+  for (int h = d; h < Hi; h += blockDim.x) w[size_t(t) * Hi + h] = row[Di + h] * wscale;
+}
+
+cudaError_t indexer_kw_post(const float* kw, int ld, int T, int Di, int Hi, const float* ln_w, const float* ln_b,
+                            float eps, const float* cos_sin, const int* pos, int dr, float wscale, void* k, float* w,
+                            cudaStream_t s) {
+  if (T == 0) return cudaSuccess;
+  if (Di % 32 || Di > 1024 || dr % 2 || dr > Di) return cudaErrorInvalidValue;
+  cb::launch_k(indexer_kw_post_kernel, T, Di, 0, s, kw, ld, Di, Hi, ln_w, ln_b, eps, cos_sin, pos, dr, wscale,
+               reinterpret_cast<__nv_bfloat16*>(k), w);
+  return cudaGetLastError();
+}
+
+}  // namespace cb
