@@ -88,6 +88,7 @@ torch::Tensor tensor_from_ptr(int64_t p, std::vector<int64_t> shape, const std::
   else if (dtype == "int64") st = at::kLong;
   else if (dtype == "uint8") st = at::kByte;
   else if (dtype == "float8_e4m3fn") st = at::kFloat8_e4m3fn;
+  else if (dtype == "float16") st = at::kHalf;
   else TORCH_CHECK(false, "tensor_from_ptr: unsupported dtype ", dtype);
   auto opts = torch::TensorOptions().dtype(st).device(torch::kCUDA, device);
   return torch::from_blob(reinterpret_cast<void*>(p), shape, opts);

@@ -480,14 +480,18 @@ class DeepseekModel:
         pos_l = fb.pos[lo:hi]
         dp = pc.attn_dp and pc.world > 1         # attention over this rank's own sequences, all heads
         qkv = None
+        q_lat_q = None                           # fp8 rows of q_lat_l when the q-norm emitted them
         if L.wqkv_a is not None:
             with region("attn.q_proj"):
                 qkv = L.wqkv_a(h, xq=hq)                                        # [T_l, q_lora + latent_dim]
         with region("attn.q_proj"):
             if cfg.q_lora_rank > 0:
                 q_lat_raw = qkv[:, :cfg.q_lora_rank] if qkv is not None else L.wq_a(h, xq=hq)
-                q_lat_l = C.rms_norm(q_lat_raw, L.q_norm, cfg.rms_eps) if self.on_gpu else \
-                    R.rms_norm(q_lat_raw, L.q_norm, cfg.rms_eps)
+                if self.on_gpu:
+                    # the q-norm also emits the fp8 rows (1x128 UE8M0) that wq_b and the indexer's wq read
+                    q_lat_l, q_lat_q = C.rms_norm(q_lat_raw, L.q_norm, cfg.rms_eps, want_bf16=True, want_fp8=True)
+                else:
+                    q_lat_l = R.rms_norm(q_lat_raw, L.q_norm, cfg.rms_eps)
             else:
                 q_lat_l = h
         with region("attn.kv_proj"):
@@ -512,7 +516,7 @@ class DeepseekModel:
         idx_l = None
         if L.has_indexer:
             with region("attn.indexer_qk"):
-                idx_l = self.indexer_qkw(i, h, q_lat_l, pos_l)
+                idx_l = self.indexer_qkw(i, h, q_lat_l, pos_l, q_lat_q)
         q_lat_a = q_lat_l.to(self.act_dtype) if self.on_gpu else q_lat_l
         out_loc = fb.out_loc
         if dp and self.owner_kv:
@@ -552,7 +556,8 @@ class DeepseekModel:
         dq = cfg.qk_head_dim
         with region("attn.q_proj"):
             if cfg.q_lora_rank > 0:
-                q = L.wq_b(q_lat).view(T, Hl, dq)
+                # the norm's fp8 rows serve when q_lat is this rank's own (not gathered) rows
+                q = L.wq_b(q_lat, xq=q_lat_q if q_lat is q_lat_a and q_lat_a is q_lat_l else None).view(T, Hl, dq)
             else:
                 q = L.wq(q_lat).view(T, Hl, dq)
             if not self.on_gpu:
@@ -584,10 +589,10 @@ class DeepseekModel:
         z = head_bmm(o.reshape(T, Gl, L.wo_a.shape[2]).to(self.act_dtype), L.wo_a)                # [T, Gl, o_lora]
         return z.reshape(T, z.shape[1] * z.shape[2]).to(self.act_dtype).contiguous()
 
-    def indexer_qkw(self, i, h, q_lat, pos):
+    def indexer_qkw(self, i, h, q_lat, pos, q_lat_q=None):
         cfg, L = self.cfg, self.layers[i]
         T, Hi, Di, dr = h.shape[0], cfg.index_n_heads, cfg.index_head_dim, cfg.qk_rope_head_dim
-        q = L.idx_wq(q_lat).view(T, Hi, Di)
+        q = L.idx_wq(q_lat, xq=q_lat_q).view(T, Hi, Di)
         if not self.on_gpu:
             q = q.clone()
         C.rope_(q, 0, dr, self.cos_sin, pos)

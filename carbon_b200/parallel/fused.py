@@ -223,7 +223,8 @@ class FusedCtx(DistCtx):
         """EP MoE over NVLink.  Per chunk: counts to every rank -> barrier -> local layout + quantise and P2P row
         stores into the owners' expert-sorted buffers -> barrier -> owner's grouped GEMMs, whose down-projection
         epilogue stores each output row straight into its token's home-rank slot (prefill-sized calls) -> barrier ->
-        local weighted top-k sum.  Decode-sized calls keep the outputs on the owner and the homes pull them.
+        local weighted top-k sum.  Decode-sized calls keep the outputs on the owner and the homes pull them after
+        the third barrier (three barriers per call either way).
         Prefill-sized calls run as two token chunks on a communication stream and the compute stream: chunk 1's
         dispatch overlaps chunk 0's expert GEMMs, chunk 0's combine overlaps chunk 1's.  Every cross-rank barrier
         is issued on the communication stream, in the same order on every rank."""
@@ -320,15 +321,17 @@ class FusedCtx(DistCtx):
 
     def _moe_combine(self, model, m, ids, pos, wf, shared, out):
         """Home side.  Push mode: one barrier (every owner's stores into this rank's slots are done), then a local
-        weighted sum.  Pull mode: barrier, P2P loads of the outputs from the owners, barrier (owners may not reuse
-        `y` before every home has read it)."""
+        weighted sum.  Pull mode: barrier, then P2P loads of the outputs from the owners.  No barrier follows the
+        pull: an owner overwrites `y` only in the grouped GEMMs of its next call on these buffers, after that call's
+        second barrier, which every home reaches only after its first barrier and so after this pull (stream
+        order); the count matrix and the receive rows are likewise written by peers only past barriers this rank
+        reaches after its last read of them."""
         self.barrier()
         if m["push"]:
             ext().moe_combine_slots(m["slots"].local, pos, wf, shared, out)
             return
         if ids.shape[0] > 0:
             ext().moe_combine_pull(m["y"].peers, ids, pos, wf, model.E_local, shared, out)
-        self.barrier()
 
     def lm_head(self, model, y: torch.Tensor) -> torch.Tensor:
         part = model.head_w(y, out_dtype=torch.float32)                     # [n, V/world]

@@ -16,8 +16,9 @@ import torch.distributed as dist
 from ..ops._ext import ext
 
 _DT = {torch.bfloat16: "bfloat16", torch.float32: "float32", torch.int32: "int32", torch.int64: "int64",
-       torch.uint8: "uint8", torch.float8_e4m3fn: "float8_e4m3fn"}
-_SZ = {torch.bfloat16: 2, torch.float32: 4, torch.int32: 4, torch.int64: 8, torch.uint8: 1, torch.float8_e4m3fn: 1}
+       torch.uint8: "uint8", torch.float8_e4m3fn: "float8_e4m3fn", torch.float16: "float16"}
+_SZ = {torch.bfloat16: 2, torch.float16: 2, torch.float32: 4, torch.int32: 4, torch.int64: 8, torch.uint8: 1,
+       torch.float8_e4m3fn: 1}
 
 
 @dataclass

@@ -34,6 +34,13 @@ def _cfg():
                                       index_topk=4096)
 
 
+def _variant_cfg(v4):
+    """v4: True = the V4 layout, "fp8kv" = the V3 layout over the fp8 latent KV cache (the bench's cache), else V3."""
+    if v4 == "fp8kv":
+        return _cfg().replace(kv_fp8=True)
+    return _cfg_v4() if v4 else _cfg()
+
+
 def _cfg_v4():
     """The V4 layout with the same discrete-choice safeguards (all experts, no pruning top-k): latent MQA over the
     token/head all-to-all, grouped output projection (one group per rank), window, sinks, Engram on layer 1 with its
@@ -76,7 +83,7 @@ def _worker(rank, world, port, comm, q, attn_dp=False, v4=False, owner=False):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120), device_id=dev)
     ok = False
     try:
-        cfg = _cfg_v4() if v4 else _cfg()
+        cfg = _variant_cfg(v4)
         w = init_weights(cfg, seed=0)
         if comm.startswith("fused"):
             pctx = FusedCtx(rank, world, heap_bytes=1 << 30, max_tokens=1024, max_seq=512, attn_dp=attn_dp,
@@ -107,6 +114,8 @@ def _worker(rank, world, port, comm, q, attn_dp=False, v4=False, owner=False):
     # owner-only KV (each request's KV on its home rank), TP with the all-to-all output projection and DP
     ("fused", False, False, True), ("fused", True, False, True), ("fused", False, True, True),
     ("nccl", False, False, True),
+    # the bench's multi-GPU layout: TP attention + all-to-all projection, owner-only KV, fp8 latent cache
+    ("fused", False, "fp8kv", True),
     # TP attention with the row-parallel projection fused with the reduce-scatter (the earlier fused path)
     ("fused-rs", False, False, False)])
 def test_two_gpu_engine_matches_single_gpu(comm, attn_dp, v4, owner):
@@ -114,7 +123,7 @@ def test_two_gpu_engine_matches_single_gpu(comm, attn_dp, v4, owner):
     from carbon_b200.models.weights import WeightSource
     from carbon_b200.ref.model import init_weights
 
-    cfg = _cfg_v4() if v4 else _cfg()
+    cfg = _variant_cfg(v4)
     w = init_weights(cfg, seed=0)
     single = Engine(cfg, device="cuda:0", source=WeightSource(cfg, state=w), num_pages=64, page_size=64)
     hist_ref = _run_forced(single, _prompts(cfg))
