@@ -482,29 +482,43 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
 #endif
 }
 
-// out[t, h, :] = Σ_s 2^(m_s - M) O_s / Σ_s 2^(m_s - M) l_s
+// out[t, h, :] = Σ_s 2^(m_s - M) O_s / Σ_s 2^(m_s - M) l_s.  One CTA of 128 threads per (token, head): the split
+// weights are computed once, each thread then combines one float4 of the 512-wide row.
+constexpr int kMaxSplits = 128;
 __global__ void mla_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int n_splits,
                                    int H, __nv_bfloat16* __restrict__ out, const float* __restrict__ sink) {
   cb::pdl_entry();
+  __shared__ float wts[kMaxSplits];
+  __shared__ float s_inv;
   const int t = blockIdx.x, h = blockIdx.y;
-  float M = -INFINITY;
-  for (int s = 0; s < n_splits; ++s) M = fmaxf(M, part_ml[((size_t(t) * n_splits + s) * H + h) * 2]);
-  const float sk = sink ? sink[h] * 1.4426950408889634f : -INFINITY;
-  M = fmaxf(M, sk);
-  float L = sink ? exp2f(sk - M) : 0.f;
-  for (int s = 0; s < n_splits; ++s) {
-    const float* ml = part_ml + ((size_t(t) * n_splits + s) * H + h) * 2;
-    if (ml[0] != -INFINITY) L += exp2f(ml[0] - M) * ml[1];
-  }
-  const float inv = L > 0.f ? 1.f / L : 0.f;
-  for (int c = threadIdx.x; c < DL; c += blockDim.x) {
-    float acc = 0.f;
+  if (threadIdx.x == 0) {
+    float M = -INFINITY;
+    for (int s = 0; s < n_splits; ++s) M = fmaxf(M, part_ml[((size_t(t) * n_splits + s) * H + h) * 2]);
+    const float sk = sink ? sink[h] * 1.4426950408889634f : -INFINITY;
+    M = fmaxf(M, sk);
+    float L = sink ? exp2f(sk - M) : 0.f;
     for (int s = 0; s < n_splits; ++s) {
-      const float m = part_ml[((size_t(t) * n_splits + s) * H + h) * 2];
-      if (m == -INFINITY) continue;
-      acc += exp2f(m - M) * part_o[((size_t(t) * n_splits + s) * H + h) * DL + c];
+      const float* ml = part_ml + ((size_t(t) * n_splits + s) * H + h) * 2;
+      const float wv = ml[0] == -INFINITY ? 0.f : exp2f(ml[0] - M);
+      wts[s] = wv;
+      if (ml[0] != -INFINITY) L += wv * ml[1];
     }
-    out[(size_t(t) * H + h) * DL + c] = __float2bfloat16_rn(acc * inv);
+    s_inv = L > 0.f ? 1.f / L : 0.f;
+  }
+  __syncthreads();
+  const float inv = s_inv;
+  for (int c = threadIdx.x * 4; c < DL; c += blockDim.x * 4) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s = 0; s < n_splits; ++s) {
+      const float wv = wts[s];
+      if (wv == 0.f) continue;
+      const float4 o = *reinterpret_cast<const float4*>(part_o + ((size_t(t) * n_splits + s) * H + h) * DL + c);
+      acc.x += wv * o.x; acc.y += wv * o.y; acc.z += wv * o.z; acc.w += wv * o.w;
+    }
+    uint2 w2;
+    w2.x = pack_bf16x2(acc.x * inv, acc.y * inv);
+    w2.y = pack_bf16x2(acc.z * inv, acc.w * inv);
+    *reinterpret_cast<uint2*>(out + (size_t(t) * H + h) * DL + c) = w2;
   }
 }
 
@@ -612,7 +626,7 @@ cudaError_t sparse_mla_any(bool f8, const void* q, int T, int H, const void* kv,
                            cudaStream_t s, const float* sink, int D) {
   using namespace mla;
   if (T == 0) return cudaSuccess;
-  if (H > HM || H < 1 || n_splits < 1 || (D != 576 && D != 512)) return cudaErrorInvalidValue;
+  if (H > HM || H < 1 || n_splits < 1 || n_splits > kMaxSplits || (D != 576 && D != 512)) return cudaErrorInvalidValue;
   if (!encode_fn()) return cudaErrorInvalidValue;
   const int RB = f8 ? (D == 576 ? 656 : 528) : D * 2;        // bytes of one cached row
   CUtensorMap tq, tkv, tsc, tpe;

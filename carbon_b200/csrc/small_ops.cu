@@ -924,12 +924,6 @@ __global__ void __cluster_dims__(kBndCluster, 1, 1) __launch_bounds__(kBndThread
     }
   }
   // ---- B: statistics partials over this CTA's columns of stream g, 8 fn rows at a time ----
-  uint4 fnext[8];                                            // fn rows of the next group, loaded a group ahead
-  if (act) {
-#pragma unroll
-    for (int rr = 0; rr < 8; ++rr)
-      fnext[rr] = __ldg(reinterpret_cast<const uint4*>(fn + size_t(rr) * FD + size_t(g) * D + col));
-  }
   for (int r0 = 0; r0 < kBndStats; r0 += 8) {
     float acc[TT][8];
 #pragma unroll
@@ -939,12 +933,8 @@ __global__ void __cluster_dims__(kBndCluster, 1, 1) __launch_bounds__(kBndThread
     if (act) {
       uint4 fv[8];
 #pragma unroll
-      for (int rr = 0; rr < 8; ++rr) fv[rr] = fnext[rr];
-      if (r0 + 8 < kBndStats) {
-#pragma unroll
-        for (int rr = 0; rr < 8; ++rr)
-          fnext[rr] = __ldg(reinterpret_cast<const uint4*>(fn + size_t(r0 + 8 + rr) * FD + size_t(g) * D + col));
-      }
+      for (int rr = 0; rr < 8; ++rr)
+        fv[rr] = __ldg(reinterpret_cast<const uint4*>(fn + size_t(r0 + rr) * FD + size_t(g) * D + col));
 #pragma unroll
       for (int rr = 0; rr < 8; ++rr) {
         const float f[8] = {bf16_lo(fv[rr].x), bf16_hi(fv[rr].x), bf16_lo(fv[rr].y), bf16_hi(fv[rr].y),
@@ -986,13 +976,13 @@ __global__ void __cluster_dims__(kBndCluster, 1, 1) __launch_bounds__(kBndThread
   cluster_sync();                                            // every CTA's partials are visible cluster-wide
   for (int e = threadIdx.x; e < TT * (kBndStats + 1); e += kBndThreads) {
     const uint32_t a = smem_u32(&red[0][0] + e);
-    float x[kBndCluster];
-#pragma unroll
-    for (int cc = 0; cc < kBndCluster; ++cc)   // every load in flight before the first add
-      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x[cc]) : "r"(mapa_shared(a, uint32_t(cc))));
     float v = 0.f;
 #pragma unroll
-    for (int cc = 0; cc < kBndCluster; ++cc) v += x[cc];
+    for (int cc = 0; cc < kBndCluster; ++cc) {
+      float x;
+      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x) : "r"(mapa_shared(a, uint32_t(cc))));
+      v += x;
+    }
     (&tot[0][0])[e] = v;
   }
   __syncthreads();
@@ -1016,14 +1006,14 @@ __global__ void __cluster_dims__(kBndCluster, 1, 1) __launch_bounds__(kBndThread
     cv = cv / s + hc_eps;
     s = cv + __shfl_xor_sync(0xffffffffu, cv, 4);             // column sums
     s += __shfl_xor_sync(0xffffffffu, s, 8);
-    cv = __fdividef(cv, s + hc_eps);
-    for (int it = 1; it < iters; ++it) {                      // approximate divisions (2 ulp): latency-bound loop
+    cv /= (s + hc_eps);
+    for (int it = 1; it < iters; ++it) {
       s = cv + __shfl_xor_sync(0xffffffffu, cv, 1);
       s += __shfl_xor_sync(0xffffffffu, s, 2);
-      cv = __fdividef(cv, s + hc_eps);
+      cv /= (s + hc_eps);
       s = cv + __shfl_xor_sync(0xffffffffu, cv, 4);
       s += __shfl_xor_sync(0xffffffffu, s, 8);
-      cv = __fdividef(cv, s + hc_eps);
+      cv /= (s + hc_eps);
     }
     if (lane < 16) coef[i][8 + lane] = cv;
     __syncwarp();
@@ -1062,13 +1052,13 @@ __global__ void __cluster_dims__(kBndCluster, 1, 1) __launch_bounds__(kBndThread
   cluster_sync();
   if (threadIdx.x < TT) {
     const uint32_t a = smem_u32(&red2[threadIdx.x]);
-    float x[kBndCluster];
-#pragma unroll
-    for (int cc = 0; cc < kBndCluster; ++cc)
-      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x[cc]) : "r"(mapa_shared(a, uint32_t(cc))));
     float v = 0.f;
 #pragma unroll
-    for (int cc = 0; cc < kBndCluster; ++cc) v += x[cc];
+    for (int cc = 0; cc < kBndCluster; ++cc) {
+      float x;
+      asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(x) : "r"(mapa_shared(a, uint32_t(cc))));
+      v += x;
+    }
     nrm[threadIdx.x] = rsqrtf(v / float(D) + rms_eps);
   }
   __syncthreads();

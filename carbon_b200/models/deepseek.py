@@ -1077,8 +1077,11 @@ def head_bmm(x: torch.Tensor, w: torch.Tensor, tail: int = 0, out_dtype=torch.bf
     if not x.is_cuda:
         out = torch.einsum("thk,hnk->thn", x[..., :K].float(), w.float())
         return torch.cat([out, x[..., K:K + tail].float()], dim=-1) if tail else out
-    if tail:
-        return torch.cat([head_bmm(x[..., :K], w).to(out_dtype), x[..., K:K + tail].to(out_dtype)], dim=-1)
+    if tail:                            # two strided copies into the output, no concatenation
+        out = torch.empty(T, H, N + tail, dtype=out_dtype, device=x.device)
+        out[..., :N] = head_bmm(x[..., :K], w)
+        out[..., N:] = x[..., K:K + tail]
+        return out
     x = x[..., :K]
     Tp = ((T + 127) // 128) * 128
     # head-major rows, each head's block padded to 128 rows; the padding rows are never read back (every output
