@@ -59,6 +59,9 @@ def parse():
                          "(a2a) or row-parallel projection + reduce-scatter (rs)")
     ap.add_argument("--replicated-kv", action="store_true",
                     help="N>1: every rank caches every request's KV (default: only each request's home rank does)")
+    ap.add_argument("--decode-cache", default="random", choices=["random", "zeros"],
+                    help="content of the decode requests' cached context rows: random latent rows and indexer keys "
+                         "(DSA selects real, scattered keys) or the zero rows of a fresh cache")
     ap.add_argument("--kv", default="fp8", choices=["fp8", "bf16"],
                     help="latent KV cache format (fp8: 656 bytes per token and layer, bf16: 1152)")
     ap.add_argument("--attn", default="tp", choices=["tp", "dp"],
@@ -279,8 +282,10 @@ def main():
         if owner_kv:
             r.home = j // (B // world)          # B / N requests per home rank
         eng._ensure_pages(r, r.seq_len)
-        r.n_cached = ctx          # cache rows are synthetic: decode cost depends on context length, not content
+        r.n_cached = ctx          # the context rows are synthetic (not computed by a prefill)
         reqs.append(r)
+    if args.decode_cache == "random":
+        fill_cache_rows(eng, reqs, ctx, gen)
     # every decode step feeds fresh uniform-random token ids (synthetic data): routing stays as diverse as a real
     # batch's, so each step streams the weights of every expert its tokens select
     def next_ids():
@@ -370,6 +375,7 @@ def main():
                        "weights": (f"{sets} distinct MoE-layer weight sets cycled over {n_moe} MoE layers "
                                    "(every layer still runs; the full untied model needs 8 GPUs)") if tied
                        else "all layers distinct", "l2": "inputs (weights) larger than L2",
+                       "decode_cache": args.decode_cache + " context rows",
                        "kv_cache": "fp8 e4m3 latent rows, UE8M0 per 64 dims + fp16 RoPE key (656 B/token/layer)"
                        if cfg.kv_fp8 else "bf16 latent rows (1152 B/token/layer)",
                        "init_s": round(init_s, 1)},
@@ -377,6 +383,29 @@ def main():
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()
+
+
+def fill_cache_rows(eng, reqs, ctx, gen):
+    """Random context rows for the decode requests this rank holds: latent rows ~N(0, 1) (the scale of RMSNorm'd
+    latents) and indexer keys, written through the cache's own store path, so the DSA indexer selects real, scattered
+    keys and the attention gathers them.  One block of rows is generated and written into every layer."""
+    from carbon_b200.engine.pd import request_slots
+
+    cache, cfg = eng.cache, eng.cfg
+    mine = [r for r in reqs if not eng.owner_kv or r.home == eng.model.pctx.rank]
+    if not mine:
+        return
+    g = torch.Generator(device=eng.device).manual_seed(int(torch.randint(0, 1 << 30, (1,), generator=gen)))
+    for r in mine:
+        slots = request_slots(eng, r, ctx).to(torch.int32)
+        rows = torch.randn(ctx, cfg.latent_dim, generator=g, device=eng.device).to(torch.bfloat16)
+        keys = torch.randn(ctx, cfg.index_head_dim, generator=g, device=eng.device).to(torch.bfloat16)
+        for layer in range(cfg.n_layers):
+            cache.write_latent(layer, slots, rows)
+            if cache.index_k and cache.index_k[layer] is not None:
+                cache.write_index_k(layer, slots, keys)
+    if eng.device.type == "cuda":
+        torch.cuda.synchronize()
 
 
 def pctx_name(p, world, owner_kv=False):

@@ -64,3 +64,38 @@ def test_tracing_on_cpu_and_chrome_trace(tmp_path):
     ev = json.loads(path.read_text())["traceEvents"]
     assert n == len(ev) == len(t.events) > 0
     assert all(e["ph"] == "X" and e["dur"] >= 0 and e["ts"] >= 0 for e in ev)
+
+
+def test_bench_fills_decode_context_rows():
+    """The bench's random decode context: every held request's slots get nonzero latent rows (through the cache's own
+    store path, fp8 rows here) and indexer keys, in every layer; slots of other requests stay untouched."""
+    import importlib.util
+    import os
+
+    import torch
+
+    from carbon_b200.config import tiny_config
+    from carbon_b200.engine.engine import Engine
+    from carbon_b200.engine.pd import request_slots
+    from carbon_b200.models.weights import WeightSource
+
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "bench.py")
+    spec = importlib.util.spec_from_file_location("carbon_bench_fill", path)
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    cfg = tiny_config().replace(kv_fp8=True)
+    eng = Engine(cfg, device="cpu", source=WeightSource(cfg, seed=0), num_pages=16, page_size=16)
+    ctx = 40
+    reqs = []
+    for _ in range(2):
+        r = eng.add_request(list(range(ctx)))
+        eng._ensure_pages(r, ctx)
+        reqs.append(r)
+    bench.fill_cache_rows(eng, reqs[:1], ctx, torch.Generator().manual_seed(0))
+    s0, s1 = request_slots(eng, reqs[0], ctx), request_slots(eng, reqs[1], ctx)
+    for layer in range(cfg.n_layers):
+        lat = eng.cache.latent[layer]
+        assert bool((lat[s0].float().abs().sum(dim=1) > 0).all())
+        assert bool((lat[s1] == 0).all())
+        if eng.cache.index_k and eng.cache.index_k[layer] is not None:
+            assert bool((eng.cache.index_k[layer][s0].abs().sum(dim=1) > 0).all())
