@@ -192,6 +192,21 @@ void mhc_boundary_small(torch::Tensor X, c10::optional<torch::Tensor> out, c10::
   if (q.has_value()) CK(cb::sf_pad(reinterpret_cast<uint32_t*>(sf->data_ptr()), T, D, cur_stream()));
 }
 
+// per-head matmul of a decode batch: x [T, H, >= K + tail] bf16, w [H, N, K] bf16 -> out [T, H, N + tail]
+void head_bmm(torch::Tensor x, torch::Tensor w, int64_t tail, torch::Tensor out, c10::optional<torch::Tensor> status) {
+  CHECK_CUDA(x); CHECK_DT(x, at::kBFloat16); CHECK_DT(w, at::kBFloat16); CHECK_CONTIG(w);
+  TORCH_CHECK(x.dim() == 3 && w.dim() == 3 && out.dim() == 3 && x.stride(2) == 1 && out.stride(2) == 1,
+              "head_bmm: x [T, H, K], w [H, N, K], out [T, H, N + tail]");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 || out.scalar_type() == at::kHalf, "head_bmm: bf16 or fp16 out");
+  const int T = x.size(0), H = x.size(1), N = w.size(1), K = w.size(2);
+  TORCH_CHECK(w.size(0) == H && x.size(2) >= K + tail && out.size(0) == T && out.size(1) == H &&
+              out.size(2) == N + tail, "head_bmm: shapes");
+  c10::cuda::CUDAGuard g(x.device());
+  CK(cb::head_bmm(x.data_ptr(), x.stride(0), x.stride(1), w.data_ptr(), T, H, N, K, out.data_ptr(),
+                  out.scalar_type() == at::kHalf, out.stride(0), out.stride(1), int(tail), ptr_or_null<int>(status),
+                  cur_stream()));
+}
+
 // DSA indexer key / head-weight post-processing (LayerNorm + RoPE of the key, scaled head weights) in one launch
 void indexer_kw_post(torch::Tensor kw, int64_t Di, torch::Tensor ln_w, torch::Tensor ln_b, double eps,
                      torch::Tensor cos_sin, torch::Tensor pos, int64_t dr, double wscale, torch::Tensor k,
@@ -499,6 +514,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("mhc_pre_norm", &mhc_pre_norm);
   m.def("mhc_boundary_small", &mhc_boundary_small);
   m.def("indexer_kw_post", &indexer_kw_post);
+  m.def("head_bmm", &head_bmm);
   m.def("mhc_post_mix", &mhc_post_mix);
   m.def("embed_hc", &embed_hc);
   m.def("row_sumsq", &row_sumsq);

@@ -37,6 +37,12 @@ cudaError_t mhc_pre_norm(const void* X, const float* pre, const float* w, int T,
                          uint32_t* sf, const int* rows, cudaStream_t s);
 // DSA indexer post-processing of the fused [wk | weights_proj] fp32 projection kw [T, ld >= Di + Hi]: k [T, Di] bf16
 // = RoPE(LayerNorm(kw[:, :Di])) (RoPE on dims [0, dr)), w [T, Hi] fp32 = kw[:, Di:] * wscale
+// Per-head matmul for decode batches (swap-AB tcgen05): out[t, h, n] = sum_k x[t, h, k] w[h, n, k] for n < N, then
+// out[t, h, N + j] = x[t, h, K + j] for j < tail.  x bf16 (strides xs_t, xs_h; unit stride along k), w bf16
+// [H, N, K] contiguous, out bf16 or fp16 (strides os_t, os_h).  T <= 256, N % 128 == 0, K % 64 == 0.
+cudaError_t head_bmm(const void* x, long long xs_t, long long xs_h, const void* w, int T, int H, int N, int K,
+                     void* out, bool out_f16, long long os_t, long long os_h, int tail, int* status, cudaStream_t s);
+int head_bmm_smem_bytes(int T, int K);
 cudaError_t indexer_kw_post(const float* kw, int ld, int T, int Di, int Hi, const float* ln_w, const float* ln_b,
                             float eps, const float* cos_sin, const int* pos, int dr, float wscale, void* k, float* w,
                             cudaStream_t s);

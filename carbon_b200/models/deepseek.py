@@ -17,6 +17,7 @@ rank every collective is the identity.
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass, field
 from typing import Dict, List, Optional
 
@@ -1077,6 +1078,12 @@ def head_bmm(x: torch.Tensor, w: torch.Tensor, tail: int = 0, out_dtype=torch.bf
     if not x.is_cuda:
         out = torch.einsum("thk,hnk->thn", x[..., :K].float(), w.float())
         return torch.cat([out, x[..., K:K + tail].float()], dim=-1) if tail else out
+    if _head_bmm_direct(x, w, tail, out_dtype):
+        # decode batch: one swap-AB tcgen05 launch reads the token rows in place and writes [T, H, N + tail]
+        from ..ops._ext import ext
+        out = torch.empty(T, H, N + tail, dtype=out_dtype, device=x.device)
+        ext().head_bmm(x, w, tail, out, None)
+        return out
     if tail:                            # two strided copies into the output, no concatenation
         out = torch.empty(T, H, N + tail, dtype=out_dtype, device=x.device)
         out[..., :N] = head_bmm(x[..., :K], w)
@@ -1097,4 +1104,17 @@ def head_bmm(x: torch.Tensor, w: torch.Tensor, tail: int = 0, out_dtype=torch.bf
     return out.view(H, Tp, N)[:, :T].transpose(0, 1)
 
 
+def _head_bmm_direct(x: torch.Tensor, w: torch.Tensor, tail: int, out_dtype) -> bool:
+    """Whether the decode-batch kernel takes this per-head matmul: at most 256 tokens, 128-multiple N, 64-multiple K,
+    bf16 operands with 16-byte aligned rows (its tensor maps), bf16 / fp16 output.  CARBON_HEAD_BMM=0 turns it off
+    (the grouped-GEMM path over head-major copies then runs)."""
+    T, H, Kx = x.shape
+    N, K = w.shape[1], w.shape[2]
+    return (_HEAD_BMM_ON and 0 < T <= 256 and N % 128 == 0 and K % 64 == 0 and x.dtype == torch.bfloat16
+            and w.dtype == torch.bfloat16 and w.is_contiguous() and x.stride(2) == 1 and x.stride(1) % 8 == 0
+            and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0 and out_dtype in (torch.bfloat16, torch.float16)
+            and Kx >= K + tail)
+
+
+_HEAD_BMM_ON = os.environ.get("CARBON_HEAD_BMM", "1") != "0"
 _HEAD_BLOCKS: Dict[tuple, torch.Tensor] = {}      # expert (= head) of each 128-row block, per (heads, blocks, device)

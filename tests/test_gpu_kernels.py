@@ -531,3 +531,33 @@ def test_indexer_kw_post_vs_torch(T):
     torch.cuda.synchronize()
     assert torch.allclose(w, kw[:, Di:] * 0.01)
     assert rel_err(k, ref_k.view(T, Di)) < 5e-3, rel_err(k, ref_k.view(T, Di))
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# per-head matmul of decode batches (swap-AB tcgen05)
+# ----------------------------------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("T,H,N,K,xw,tail,odt", [
+    (32, 128, 512, 128, 192, 64, torch.float16),     # MLA query absorption: q [T, H, 192] -> [q_nope W_uk | q_rope]
+    (32, 128, 512, 128, 192, 64, torch.bfloat16),
+    (32, 128, 128, 512, 512, 0, torch.bfloat16),     # value un-absorption: o_lat [T, H, 512] -> [T, H, 128]
+    (1, 16, 512, 128, 192, 64, torch.bfloat16),
+    (200, 16, 512, 128, 192, 64, torch.float16),
+    (256, 16, 128, 512, 512, 0, torch.bfloat16),
+    (7, 8, 256, 192, 256, 0, torch.bfloat16),
+])
+def test_head_bmm_decode_vs_fp32(T, H, N, K, xw, tail, odt):
+    from carbon_b200.models.deepseek import _head_bmm_direct, head_bmm
+
+    torch.manual_seed(0)
+    x = torch.randn(T, H, xw, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(H, N, K, device=DEV) * 0.05).to(torch.bfloat16)
+    assert _head_bmm_direct(x, w, tail, odt)
+    launches = _ext().launch_count()
+    out = head_bmm(x, w, tail=tail, out_dtype=odt)
+    torch.cuda.synchronize()
+    assert _ext().launch_count() == launches + 1                   # one launch, no staging copies
+    ref = torch.einsum("thk,hnk->thn", x[..., :K].float(), w.float())
+    assert out.shape == (T, H, N + tail) and out.dtype == odt
+    assert rel_err(out[..., :N], ref) < 4e-3
+    if tail:
+        assert torch.equal(out[..., N:].float().cpu(), x[..., K:K + tail].to(odt).float().cpu())
