@@ -166,6 +166,19 @@ CB_DEVICE void pdl_entry() {
 #endif
 }
 
+// The two halves of pdl_entry(), for kernels that start work which does not depend on the previous kernel (weight
+// loads) before waiting: every thread that reads the previous kernel's output must have executed pdl_wait() first.
+CB_DEVICE void pdl_wait() {
+#if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 900
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+#endif
+}
+CB_DEVICE void pdl_launch_dependents() {
+#if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 900
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+#endif
+}
+
 // Whether launches carry the programmatic-serialization attribute (CARBON_PDL=0 turns it off).
 inline bool pdl_enabled() {
   static int v = -1;

@@ -123,6 +123,22 @@ static cudaError_t splitk_reduce(const float* part, int splits, int M, int N, in
   return cudaGetLastError();
 }
 
+// Sum of the float4 at p in `splits` consecutive slabs (stride `slab` floats), added in split order; the loads of up
+// to 8 splits are issued before any is used, so a reduction costs one memory latency per 8 splits, not one per split.
+CB_DEVICE float4 splits_sum4(const float* __restrict__ p, size_t slab, int splits) {
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int sp0 = 0; sp0 < splits; sp0 += 8) {
+    float4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (sp0 + j < splits) v[j] = *reinterpret_cast<const float4*>(p + size_t(sp0 + j) * slab);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (sp0 + j < splits) { acc.x += v[j].x; acc.y += v[j].y; acc.z += v[j].z; acc.w += v[j].w; }
+  }
+  return acc;
+}
+
 // Split-K partial slabs [splits][M][N] (fp32) -> output.  MODE 0: fp32, MODE 1: bf16; 4 columns per thread.
 template <int MODE>
 __global__ void splitk_reduce_out_kernel(const float* __restrict__ part, int splits, int M, int N, void* out,
@@ -131,11 +147,7 @@ __global__ void splitk_reduce_out_kernel(const float* __restrict__ part, int spl
   const int64_t total4 = int64_t(M) * (N / 4);
   for (int64_t i = blockIdx.x * int64_t(blockDim.x) + threadIdx.x; i < total4; i += int64_t(gridDim.x) * blockDim.x) {
     const int r = int(i / (N / 4)), c = int(i % (N / 4)) * 4;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int sp = 0; sp < splits; ++sp) {
-      const float4 v = *reinterpret_cast<const float4*>(part + (size_t(sp) * M + r) * N + c);
-      acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
-    }
+    const float4 acc = splits_sum4(part + size_t(r) * N + c, size_t(M) * N, splits);
     if (MODE == 0) {
       *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + size_t(r) * ldo + c) = acc;
     } else {
@@ -152,15 +164,14 @@ CB_DEVICE void swiglu_reduce_row(const float* __restrict__ part, int splits, int
                                  int row, int g, int lane) {
   float a[4];
   float amax = 0.f;
+  // gate and up sums of this lane's 4 columns (float4 loads, every split's load in flight before the adds)
+  const float* pr = part + size_t(row) * N + 256 * g + 4 * lane;
+  const float4 g4 = splits_sum4(pr, size_t(M) * N, splits);
+  const float4 u4 = splits_sum4(pr + 128, size_t(M) * N, splits);
+  const float gs[4] = {g4.x, g4.y, g4.z, g4.w}, us[4] = {u4.x, u4.y, u4.z, u4.w};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const int t = 4 * lane + i;
-    float gv = 0.f, uv = 0.f;
-    for (int sp = 0; sp < splits; ++sp) {
-      const float* pr = part + (size_t(sp) * M + row) * N + 256 * g;
-      gv += pr[t];
-      uv += pr[128 + t];
-    }
+    float gv = gs[i], uv = us[i];
     if (limit > 0.f) { gv = fminf(gv, limit); uv = fminf(fmaxf(uv, -limit), limit); }
     a[i] = gv / (1.f + __expf(-gv)) * uv;
     amax = fmaxf(amax, fabsf(a[i]));
@@ -391,11 +402,18 @@ cudaError_t gemm_bf16(const void* A, int lda, const void* B, int ldb, int M, int
       if (m_block_expert || !work) return cudaErrorInvalidValue;
       p.k_splits = k_splits;
       p.out = work;
+      const bool vec = (N % 4) == 0 && (ldo % 4) == 0;
+      if (vec) p.ldo = N;                                              // dense [splits, M, N] slabs
       cudaError_t e = launch<KIND_BF16, EPI_F32, 128, 6, 2>(ta, tb, p, max_tiles * k_splits, num_sms, s);
       if (e != cudaSuccess) return e;
       const int nk_total = ceil_div(K, 64), nk_per = ceil_div(ceil_div(nk_total, k_splits), 4) * 4;
       const int used = ceil_div(nk_total, nk_per);                     // splits that own at least one k-block
-      return splitk_reduce(work, used, M, N, ldo, reinterpret_cast<float*>(out), s);
+      if (!vec) return splitk_reduce(work, used, M, N, ldo, reinterpret_cast<float*>(out), s);
+      const int64_t total4 = int64_t(M) * (N / 4);
+      const int blocks = int(total4 / 256 + 1 < 1024 ? total4 / 256 + 1 : 1024);
+      cb::launch_k(splitk_reduce_out_kernel<0>, blocks, 256, 0, s, static_cast<const float*>(work), used, M, N, out,
+                   ldo);
+      return cudaGetLastError();
     }
     return launch<KIND_BF16, EPI_F32, 128, 6, 2>(ta, tb, p, max_tiles, num_sms, s);
   }

@@ -67,10 +67,35 @@ struct GemmSmem {
   static constexpr int SFB_BYTES = (BLOCK_N / 128) * 512;
 };
 
+// Dense GEMMs: L2 prefetch of the B (weight) boxes of this CTA's first work item, up to one ring of k-blocks,
+// issued before the kernel waits for its predecessor (programmatic dependent launch), so the weight stream of a
+// decode-size GEMM starts while the previous kernel still runs.  The tile arithmetic is tile_coords' below.
+template <int BLOCK_N, int STAGES, int BLOCK_K, bool SPLIT>
+__device__ __forceinline__ void gemm_prefetch_first_b(const CUtensorMap* tmap_b, const GemmParams& p) {
+#if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 1000
+  constexpr int GROUP_M = 16;
+  const int num_mb = ceil_div(p.M, 128), num_nb = ceil_div(p.N, BLOCK_N);
+  const int ksplit = (SPLIT && p.k_splits > 1) ? p.k_splits : 1;
+  const int t = int(blockIdx.x);
+  if (t >= num_mb * num_nb * ksplit) return;
+  const int tt = t / ksplit;
+  const int per_group = GROUP_M * num_nb;
+  const int g = tt / per_group, r = tt - g * per_group;
+  const int rows = min(GROUP_M, num_mb - g * GROUP_M);
+  const int nb = r / rows;
+  const int nk_total = ceil_div(p.K, BLOCK_K);
+  const int nk_per = ceil_div(ceil_div(nk_total, ksplit), 4) * 4;
+  const int kb0 = (t % ksplit) * nk_per, kb1 = min(nk_total, min(kb0 + nk_per, kb0 + STAGES));
+  for (int kb = kb0; kb < kb1; ++kb) tma_prefetch_l2_2d(tmap_b, kb * BLOCK_K, nb * BLOCK_N);
+#endif
+}
+
 template <int KIND, int EPI, int BLOCK_N, int STAGES, int ACC_STAGES>
 __global__ void __launch_bounds__(256, 1) gemm_tc_kernel(const __grid_constant__ CUtensorMap tmap_a,
                                                          const __grid_constant__ CUtensorMap tmap_b,
                                                          const GemmParams p) {
+  if (threadIdx.x == 0 && p.m_block_expert == nullptr)
+    gemm_prefetch_first_b<BLOCK_N, STAGES, (KIND == KIND_MXF8 ? 128 : 64), EPI == EPI_F32>(&tmap_b, p);
   cb::pdl_entry();
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 1000
   using S = GemmSmem<BLOCK_N>;

@@ -23,6 +23,7 @@
 #include <cudaTypedefs.h>
 #include <algorithm>
 #include <mutex>
+#include <type_traits>
 #include "ptx.cuh"
 #include "small_ops.h"
 
@@ -32,7 +33,8 @@ namespace hb {
 constexpr int BM = 128;                 // weight rows (output columns n) per CTA
 constexpr int BK = 64;                  // bf16 elements per 128-byte swizzle row
 constexpr int TILE_A = BM * 128;        // bytes of one A stage
-constexpr int kMaxStages = 4;
+constexpr int kMaxStages = 8;
+constexpr int kStageBudget = 200 * 1024;   // shared memory for the stage ring (every K chunk in flight when it fits)
 constexpr int kThreads = 128;
 constexpr int kMaxT = 256;
 
@@ -58,7 +60,6 @@ struct Args {
 template <typename OutT>
 __global__ void __launch_bounds__(kThreads) head_bmm_kernel(const __grid_constant__ CUtensorMap tw,
                                                              const __grid_constant__ CUtensorMap tx, const Args a) {
-  cb::pdl_entry();
 #if defined(__CUDA_ARCH__) && __CUDA_ARCH__ >= 1000
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -94,18 +95,35 @@ __global__ void __launch_bounds__(kThreads) head_bmm_kernel(const __grid_constan
     *abort_flag = 1;
   };
 
+  // The weights do not depend on the previous kernel: the first ring's weight tiles are requested before waiting
+  // for it (programmatic dependent launch), the token rows after.
+  const int pre = nk < stages ? nk : stages;
   if (warp == 0) {
     if (elect_one()) {
+      for (int kb = 0; kb < pre; ++kb) {
+        mbar_arrive_expect_tx(&full[kb], uint32_t(TILE_A) + tile_b);
+        tma_load_2d(sA + kb * TILE_A, &tw, &full[kb], kb * BK, h * a.N + nb * BM);
+      }
+      pdl_wait();
       for (int kb = 0; kb < nk && !*abort_flag; ++kb) {
         const int s = kb % stages;
         const uint32_t ph = uint32_t(kb / stages) & 1u;
-        if (!mbar_wait(&empty[s], ph ^ 1u)) { fail(kErrTimeoutEmpty); break; }
-        mbar_arrive_expect_tx(&full[s], uint32_t(TILE_A) + tile_b);
-        tma_load_2d(sA + s * TILE_A, &tw, &full[s], kb * BK, h * a.N + nb * BM);
+        if (kb >= pre) {
+          if (!mbar_wait(&empty[s], ph ^ 1u)) { fail(kErrTimeoutEmpty); break; }
+          mbar_arrive_expect_tx(&full[s], uint32_t(TILE_A) + tile_b);
+          tma_load_2d(sA + s * TILE_A, &tw, &full[s], kb * BK, h * a.N + nb * BM);
+        }
         tma_load_3d(sB + s * tile_b, &tx, &full[s], kb * BK, h, 0);
       }
+    } else {
+      pdl_wait();
     }
-  } else if (warp == 1) {
+    pdl_launch_dependents();
+  } else {
+    pdl_wait();
+    pdl_launch_dependents();
+  }
+  if (warp == 1) {
     if (elect_one()) {
       const uint32_t idesc = idesc_bf16(BM, a.TB);
       bool ok = true;
@@ -128,13 +146,27 @@ __global__ void __launch_bounds__(kThreads) head_bmm_kernel(const __grid_constan
   }
   __syncwarp();
 
-  // tail columns (x[..., K:K+tail] copied unchanged) while the MMAs run: CTAs of n-block 0 only
-  if (a.tail > 0 && nb == 0) {
+  // tail columns (x[..., K:K+tail] copied unchanged) while the MMAs run, spread over the head's n-block CTAs in
+  // 16-byte pieces (the host checks that rows, strides and offsets are 8-element multiples)
+  if (a.tail > 0) {
     OutT* o = reinterpret_cast<OutT*>(a.out) + size_t(h) * a.os_h + a.N;
     const __nv_bfloat16* xs = a.x + size_t(h) * a.xs_h + a.K;
-    for (int i = threadIdx.x; i < a.T * a.tail; i += kThreads) {
-      const int t = i / a.tail, j = i - t * a.tail;
-      o[size_t(t) * a.os_t + j] = cvt_out<OutT>(__bfloat162float(xs[size_t(t) * a.xs_t + j]));
+    const int per_row = a.tail / 8, items = a.T * per_row;
+    for (int i = nb * kThreads + threadIdx.x; i < items; i += gridDim.x * kThreads) {
+      const int t = i / per_row, j = (i - t * per_row) * 8;
+      const uint4 v = *reinterpret_cast<const uint4*>(xs + size_t(t) * a.xs_t + j);
+      uint4 r = v;
+      if constexpr (sizeof(OutT) == 2 && !std::is_same<OutT, __nv_bfloat16>::value) {
+        const uint32_t in[4] = {v.x, v.y, v.z, v.w};
+        uint32_t outw[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const __half2 hv = __floats2half2_rn(bf16_lo(in[e]), bf16_hi(in[e]));
+          outw[e] = *reinterpret_cast<const uint32_t*>(&hv);
+        }
+        r = make_uint4(outw[0], outw[1], outw[2], outw[3]);
+      }
+      *reinterpret_cast<uint4*>(o + size_t(t) * a.os_t + j) = r;
     }
   }
 
@@ -191,12 +223,18 @@ static bool encode(CUtensorMap* m, const void* ptr, int rank, const cuuint64_t* 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// stage count: every K chunk in flight at once when the ring fits the budget, at least one stage
+static int head_bmm_stages(int tb, int K) {
+  const int per = TILE_A + tb * 128;
+  return std::max(1, std::min({kMaxStages, K / BK, kStageBudget / per}));
+}
+
 }  // namespace hb
 
 int head_bmm_smem_bytes(int T, int K) {
   using namespace hb;
   const int tb = ((T + 15) / 16) * 16;
-  const int stages = std::min(kMaxStages, std::max(1, K / BK));
+  const int stages = head_bmm_stages(tb, K);
   const int need = 1024 + stages * (TILE_A + tb * 128) + 8 * (2 * kMaxStages + 1) + 16;
   // a floor that admits at most 512 / cols CTAs per SM, so every resident CTA's TMEM allocation succeeds at once
   const int floor_bytes = tmem_cols_for(tb) * 454;
@@ -208,13 +246,15 @@ cudaError_t head_bmm(const void* x, long long xs_t, long long xs_h, const void* 
                      cudaStream_t s) {
   using namespace hb;
   if (T <= 0 || H <= 0) return cudaSuccess;
-  if (T > kMaxT || N % BM || K % BK || K <= 0 || tail < 0) return cudaErrorInvalidValue;
+  if (T > kMaxT || N % BM || K % BK || K <= 0 || tail < 0 || tail % 8 || xs_t % 8 || xs_h % 8 || os_t % 8 ||
+      os_h % 8 || (reinterpret_cast<uintptr_t>(out) & 15))
+    return cudaErrorInvalidValue;
   Args a;
   a.T = T;
   a.TB = ((T + 15) / 16) * 16;
   a.N = N;
   a.K = K;
-  a.stages = std::min(kMaxStages, K / BK);
+  a.stages = head_bmm_stages(a.TB, K);
   a.out = out;
   a.os_t = os_t;
   a.os_h = os_h;

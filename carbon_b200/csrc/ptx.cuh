@@ -120,6 +120,13 @@ CB_DEVICE void tma_load_3d(void* smem_dst, const void* tmap, uint64_t* bar, int 
 }
 
 // Contiguous global -> shared copy completing on an mbarrier. Both addresses 16-byte aligned, bytes % 16 == 0.
+// L2 prefetch of one tensor-map box (no shared memory, no barrier).  L2 is the device's point of coherence, so a
+// prefetch issued before the previous kernel's writes land cannot make a later load see stale data.
+CB_DEVICE void tma_prefetch_l2_2d(const void* tmap, int c0, int c1) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];"
+               ::"l"(reinterpret_cast<uint64_t>(tmap)), "r"(c0), "r"(c1) : "memory");
+}
+
 CB_DEVICE void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
   asm volatile(
       "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"

@@ -1106,14 +1106,14 @@ def head_bmm(x: torch.Tensor, w: torch.Tensor, tail: int = 0, out_dtype=torch.bf
 
 def _head_bmm_direct(x: torch.Tensor, w: torch.Tensor, tail: int, out_dtype) -> bool:
     """Whether the decode-batch kernel takes this per-head matmul: at most 256 tokens, 128-multiple N, 64-multiple K,
-    bf16 operands with 16-byte aligned rows (its tensor maps), bf16 / fp16 output.  CARBON_HEAD_BMM=0 turns it off
+    8-multiple tail, bf16 operands with 16-byte aligned rows (its tensor maps), bf16 / fp16 output.  CARBON_HEAD_BMM=0 turns it off
     (the grouped-GEMM path over head-major copies then runs)."""
     T, H, Kx = x.shape
     N, K = w.shape[1], w.shape[2]
     return (_HEAD_BMM_ON and 0 < T <= 256 and N % 128 == 0 and K % 64 == 0 and x.dtype == torch.bfloat16
             and w.dtype == torch.bfloat16 and w.is_contiguous() and x.stride(2) == 1 and x.stride(1) % 8 == 0
             and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0 and out_dtype in (torch.bfloat16, torch.float16)
-            and Kx >= K + tail)
+            and Kx >= K + tail and tail % 8 == 0)
 
 
 _HEAD_BMM_ON = os.environ.get("CARBON_HEAD_BMM", "1") != "0"

@@ -69,12 +69,24 @@ def bf16_gemm(a: torch.Tensor, b: torch.Tensor, out_dtype=torch.bfloat16, out: O
     if k_splits == 0:
         k_splits = 1
         if epi == OUT_F32 and m_block_expert is None:
+            # decode-sized rows: split K until the tiles x splits work items fill the SMs once (whole 4-block
+            # k-groups per split); the weight stream is then read by one CTA per SM instead of a handful
             tiles = ((M + 127) // 128) * ((N + 127) // 128)
             kblocks = (a.shape[1] + 63) // 64
             if tiles < 32 and kblocks >= 64:
-                k_splits = max(1, min(kblocks // 16, 128 // tiles))
+                k_splits = max(1, min(kblocks // 4, _num_sms(a.device) // tiles))
     ext().gemm_bf16(a, b, out, epi, m_block_expert, num_m_blocks, n_per_group, status, k_splits)
     return out
+
+
+_SMS = {}
+
+
+def _num_sms(device: torch.device) -> int:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _SMS:
+        _SMS[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return _SMS[idx]
 
 
 def interleave_gate_up(w1: torch.Tensor, w3: torch.Tensor, chunk: int = 128) -> torch.Tensor:
