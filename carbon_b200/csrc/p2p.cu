@@ -224,44 +224,75 @@ cudaError_t moe_count(const int* ids, int Tk, int E, int world, int my_rank, con
 // after the count barrier).  Owner o holds experts [o*El, (o+1)*El); each expert's segment is padded to `align`
 // rows.  my_off[e]: the row of expert e's segment at its owner where this rank's rows start (sources in rank order).
 // For this rank's own experts: m_block_expert (expert of each 128-row block, -1 beyond) and num_blocks.
-// One thread per owner walks its El experts.
+// One thread per global expert: its row count over all sources and the rows of lower-ranked sources, then a
+// block-wide inclusive scan of the 128-row block counts; each owner's segment starts at row 0 of its buffer.
 __global__ void moe_layout_kernel(const int* __restrict__ cnt, int world, int E, int my_rank, int max_blocks,
                                   int align, int* __restrict__ my_off, int* __restrict__ m_block_expert,
                                   int* __restrict__ num_blocks) {
   cb::pdl_entry();
-  const int o = threadIdx.x;
-  if (o >= world) return;
+  __shared__ int s_incl[1024];
+  __shared__ int s_warp[32];
+  const int e = threadIdx.x;
+  const int lane = e & 31, wid = e >> 5, nw = blockDim.x >> 5;
   const int El = E / world;
-  int acc = 0, b = 0;
-  for (int el = 0; el < El; ++el) {
-    const int e = o * El + el;
-    int n = 0, before = 0;
+  int n = 0, before = 0;
+  if (e < E) {
+#pragma unroll 8
     for (int sr = 0; sr < world; ++sr) {
       const int c = cnt[sr * E + e];
       if (sr < my_rank) before += c;
       n += c;
     }
-    my_off[e] = acc + before;
-    const int nb = (n + align - 1) / align * (align / 128);   // 128-row blocks, segment padded to `align` rows
+  }
+  const int nb = e < E ? (n + align - 1) / align * (align / 128) : 0;   // segment padded to `align` rows
+  int v = nb;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += u;
+  }
+  if (lane == 31) s_warp[wid] = v;
+  __syncthreads();
+  if (wid == 0) {
+    int x = lane < nw ? s_warp[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += u;
+    }
+    if (lane < nw) s_warp[lane] = x;
+  }
+  __syncthreads();
+  const int incl = v + (wid > 0 ? s_warp[wid - 1] : 0);
+  if (e < E) s_incl[e] = incl;
+  __syncthreads();
+  const int mine0 = my_rank * El, mine1 = mine0 + El;
+  const int mine_base = mine0 > 0 ? s_incl[mine0 - 1] : 0;
+  const int total = s_incl[mine1 - 1] - mine_base;              // 128-row blocks of this rank's experts
+  if (e < E) {
+    const int o = e / El;
+    const int seg_base = o * El > 0 ? s_incl[o * El - 1] : 0;
+    const int local = incl - nb - seg_base;                      // blocks before e inside its owner's buffer
+    my_off[e] = local * 128 + before;
     if (o == my_rank)
-      for (int j = 0; j < nb && b < max_blocks; ++j) m_block_expert[b++] = el;
-    acc += nb * 128;
+      for (int j = 0; j < nb && local + j < max_blocks; ++j) m_block_expert[local + j] = e - mine0;
   }
-  if (o == my_rank) {
-    num_blocks[0] = b;
-    for (int j = b; j < max_blocks; ++j) m_block_expert[j] = -1;
-  }
+  for (int j = total + e; j < max_blocks; j += blockDim.x) m_block_expert[j] = -1;
+  if (e == 0) num_blocks[0] = total < max_blocks ? total : max_blocks;
 }
 
 cudaError_t moe_layout(const int* cnt, int world, int E, int my_rank, int max_blocks, int align, int* my_off,
                        int* m_block_expert, int* num_blocks, cudaStream_t s) {
-  if ((align != 128 && align != 256) || world > 1024 || E % world) return cudaErrorInvalidValue;
-  cb::launch_k(moe_layout_kernel, 1, ((world + 31) / 32) * 32, 0, s, cnt, world, E, my_rank, max_blocks, align, my_off,
+  if ((align != 128 && align != 256) || world > 1024 || E % world || E > 1024) return cudaErrorInvalidValue;
+  cb::launch_k(moe_layout_kernel, 1, ((E + 31) / 32) * 32, 0, s, cnt, world, E, my_rank, max_blocks, align, my_off,
                                                            m_block_expert, num_blocks);
   return cudaGetLastError();
 }
 
-// Dispatch: one CTA (256 threads) per local token; the row is quantised once (1x128 UE8M0 blocks), then written to
+constexpr int kDispatchCols = 1024;      // columns of a token row per dispatch CTA (a multiple of 512)
+constexpr int kSplitRowsBelow = 1024;    // token counts below this split each row over several CTAs
+
+// Dispatch: one CTA per local token (or, for decode batches, per 1024 columns of it); the row is quantised once (1x128 UE8M0 blocks), then written to
 // each selected expert's owner at row  my_off[e] + pair_rank.  Destination rows are stored in pos_out [T, k]
 // (row index inside the owner's buffer, -1 if it did not fit) for a pull combine; with rinfo_ptrs the owner also
 // learns where each received row goes back to: rinfo_owner[row] = (my_rank << 24) | (t * k + j), the slot of this
@@ -274,6 +305,8 @@ __global__ void moe_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int D, 
                                     int cap, int* __restrict__ pos_out, int* __restrict__ status) {
   cb::pdl_entry();
   const int t = blockIdx.x;
+  const int span = gridDim.y == 1 ? D : kDispatchCols;
+  const int c0 = blockIdx.y * span, c1 = min(D, c0 + span);    // this CTA's columns
   const int row_blocks = cap / 128;
   __shared__ int s_dst[16], s_owner[16];
   __shared__ uint32_t s_sf[64];            // UE8M0 scale of each 128-column block, four per word
@@ -284,15 +317,17 @@ __global__ void moe_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int D, 
     if (row >= cap) { if (status) atomicCAS(status, 0, kErrBadArg); row = -1; }
     s_dst[threadIdx.x] = row;
     s_owner[threadIdx.x] = owner;
-    pos_out[t * k + threadIdx.x] = row;
-    if (rinfo_ptrs && row >= 0)
-      reinterpret_cast<int*>(rinfo_ptrs[owner])[row] = (my_rank << 24) | (t * k + threadIdx.x);
+    if (blockIdx.y == 0) {
+      pos_out[t * k + threadIdx.x] = row;
+      if (rinfo_ptrs && row >= 0)
+        reinterpret_cast<int*>(rinfo_ptrs[owner])[row] = (my_rank << 24) | (t * k + threadIdx.x);
+    }
   }
   if (threadIdx.x < 64) s_sf[threadIdx.x] = 0x7f7f7f7fu;
   __syncthreads();
   // each group of 16 threads quantises one 128-column block (8 values per thread); every warp store writes 256
   // contiguous bytes of a destination row
-  for (int col = threadIdx.x * 8; col < D; col += blockDim.x * 8) {
+  for (int col = c0 + threadIdx.x * 8; col < c1; col += blockDim.x * 8) {
     const uint4 raw = *reinterpret_cast<const uint4*>(x + size_t(t) * D + col);
     float v[8] = {bf16_lo(raw.x), bf16_hi(raw.x), bf16_lo(raw.y), bf16_hi(raw.y),
                   bf16_lo(raw.z), bf16_hi(raw.z), bf16_lo(raw.w), bf16_hi(raw.w)};
@@ -317,9 +352,9 @@ __global__ void moe_dispatch_kernel(const __nv_bfloat16* __restrict__ x, int D, 
   }
   __syncthreads();
   // scale words: word g of a row holds the scales of column blocks 4g..4g+3 (SF tile layout of the owner)
-  const int words = (D / 128 + 3) / 4;
+  const int g0 = c0 / 512, words = (c1 + 511) / 512 - g0;       // scale words covering this CTA's columns
   for (int i = threadIdx.x; i < k * words; i += blockDim.x) {
-    const int j = i / words, g = i - j * words;
+    const int j = i / words, g = g0 + i - j * words;
     const int row = s_dst[j];
     if (row < 0) continue;
     const int rb = row >> 7, r = row & 127;
@@ -336,7 +371,12 @@ cudaError_t moe_dispatch(const void* x, int T, int D, const int* ids, int k, int
                          cudaStream_t s) {
   if (T == 0) return cudaSuccess;
   if (D % 128 || D > 64 * 512 || k > 16 || cap % 128 || (rinfo_ptrs && T * k > (1 << 24))) return cudaErrorInvalidValue;
-  cb::launch_k(moe_dispatch_kernel, T, 256, 0, s, reinterpret_cast<const __nv_bfloat16*>(x), D, ids, k, El, my_rank, pair_rank,
+  // decode batches: a token row is split over D/1024 CTAs (one 8-column chunk per thread) so the few tokens
+  // spread their peer stores over the SMs; prefill batches: one 256-thread CTA per token
+  const bool split = T < kSplitRowsBelow;
+  cb::launch_k(moe_dispatch_kernel, dim3(T, split ? (D + kDispatchCols - 1) / kDispatchCols : 1),
+               split ? kDispatchCols / 8 : 256, 0, s,
+               reinterpret_cast<const __nv_bfloat16*>(x), D, ids, k, El, my_rank, pair_rank,
                                         recv_ptrs, sf_ptrs, my_off, rinfo_ptrs, cap, pos_out, status);
   return cudaGetLastError();
 }
@@ -356,7 +396,7 @@ __global__ void moe_combine_slots_kernel(const __nv_bfloat16* __restrict__ slots
   }
   __syncthreads();
   const uint4* src = reinterpret_cast<const uint4*>(slots + size_t(t) * k * D);
-  for (int c = threadIdx.x; c < D / 8; c += blockDim.x) {
+  for (int c = blockIdx.y * blockDim.x + threadIdx.x; c < D / 8; c += gridDim.y * blockDim.x) {
     float acc[8];
     if (add) {
       const uint4 a = *reinterpret_cast<const uint4*>(add + size_t(t) * D + 8 * c);
@@ -405,7 +445,7 @@ __global__ void moe_combine_pull_kernel(const uint64_t* __restrict__ y_ptrs, int
                                         const int* __restrict__ pos, const float* __restrict__ w, int k, int El,
                                         const __nv_bfloat16* __restrict__ add, __nv_bfloat16* __restrict__ out) {
   cb::pdl_entry();
-  const int t = blockIdx.x;
+  const int t = blockIdx.x;                // token; blockIdx.y: 1024-column slice of its row
   __shared__ const uint4* s_src[KMAX];
   __shared__ float s_w[KMAX];
   if (threadIdx.x < KMAX) {
@@ -417,7 +457,7 @@ __global__ void moe_combine_pull_kernel(const uint64_t* __restrict__ y_ptrs, int
     s_w[j] = row < 0 ? 0.f : w[t * k + j];
   }
   __syncthreads();
-  for (int c = threadIdx.x; c < D / 8; c += blockDim.x) {
+  for (int c = blockIdx.y * blockDim.x + threadIdx.x; c < D / 8; c += gridDim.y * blockDim.x) {
     float acc[8];
     if (add) {
       const uint4 a = *reinterpret_cast<const uint4*>(add + size_t(t) * D + 8 * c);
@@ -450,10 +490,13 @@ cudaError_t moe_combine_pull(const uint64_t* y_ptrs, int T, int D, const int* id
   if (D % 8 || k > 16) return cudaErrorInvalidValue;
   const auto* a = reinterpret_cast<const __nv_bfloat16*>(add);
   auto* o = reinterpret_cast<__nv_bfloat16*>(out);
+  // decode batches: a token row is split over D/1024 CTAs so every SM keeps loads in flight (one column chunk per
+  // thread: its k NVLink reads are issued together); prefill batches: one CTA per token
+  const dim3 grid(T, T < kSplitRowsBelow ? (D / 8 + 127) / 128 : 1);
   if (k <= 8)
-    cb::launch_k(moe_combine_pull_kernel<8>, T, 128, 0, s, y_ptrs, D, ids, pos, w, k, El, a, o);
+    cb::launch_k(moe_combine_pull_kernel<8>, grid, 128, 0, s, y_ptrs, D, ids, pos, w, k, El, a, o);
   else
-    cb::launch_k(moe_combine_pull_kernel<16>, T, 128, 0, s, y_ptrs, D, ids, pos, w, k, El, a, o);
+    cb::launch_k(moe_combine_pull_kernel<16>, grid, 128, 0, s, y_ptrs, D, ids, pos, w, k, El, a, o);
   return cudaGetLastError();
 }
 

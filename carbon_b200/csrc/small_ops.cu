@@ -855,6 +855,13 @@ __global__ void __cluster_dims__(kBndCluster, 1, 1) __launch_bounds__(kBndThread
                               const float* __restrict__ w, __nv_bfloat16* __restrict__ y, uint8_t* __restrict__ q,
                               uint32_t* __restrict__ sf, int row_blocks, float* __restrict__ pre_out,
                               float* __restrict__ post_out, float* __restrict__ comb_out) {
+  // the statistics weights (fn) do not depend on the previous kernel: the first token group's CTAs request their
+  // column slice of all 48 rows x 4 streams into L2 before waiting for it
+  if (blockIdx.y == 0) {
+    const int cr = int(cluster_ctarank()), Dcp = D / kBndCluster;
+    for (int i = threadIdx.x; i < kBndStats * 4; i += kBndThreads)
+      bulk_prefetch_l2(fn + size_t(i >> 2) * 4 * D + size_t(i & 3) * D + size_t(cr) * Dcp, uint32_t(Dcp) * 2);
+  }
   cb::pdl_entry();
   __shared__ float xs_sm[TT][4][kBndCols * 8];                // the new streams of this CTA's columns
   __shared__ float part[kBndWarps][TT * 8];                   // per-warp partials of one 8-row group

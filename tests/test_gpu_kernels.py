@@ -561,3 +561,47 @@ def test_head_bmm_decode_vs_fp32(T, H, N, K, xw, tail, odt):
     assert rel_err(out[..., :N], ref) < 4e-3
     if tail:
         assert torch.equal(out[..., N:].float().cpu(), x[..., K:K + tail].to(odt).float().cpu())
+
+
+# ----------------------------------------------------------------------------------------------------------------------
+# EP receive-buffer layout (the count matrix of every source rank -> offsets and this rank's expert blocks)
+# ----------------------------------------------------------------------------------------------------------------------
+def _layout_ref(cnt, world, my_rank, max_blocks, align):
+    E = cnt.shape[1]
+    El = E // world
+    my_off = [0] * E
+    mbe = [-1] * max_blocks
+    total = 0
+    for o in range(world):
+        acc = b = 0
+        for el in range(El):
+            e = o * El + el
+            n = int(cnt[:, e].sum())
+            my_off[e] = acc + int(cnt[:my_rank, e].sum())
+            nb = (n + align - 1) // align * (align // 128)
+            if o == my_rank:
+                for _ in range(nb):
+                    if b < max_blocks:
+                        mbe[b] = el
+                        b += 1
+            acc += nb * 128
+        if o == my_rank:
+            total = b
+    return my_off, mbe, total
+
+
+@pytest.mark.parametrize("world,E,align,max_blocks", [(2, 256, 128, 300), (8, 256, 128, 64), (8, 256, 256, 40),
+                                                      (4, 384, 128, 7)])
+def test_moe_layout_vs_python(world, E, align, max_blocks):
+    torch.manual_seed(world * 7 + E)
+    cnt = torch.randint(0, 40, (world, E), dtype=torch.int32)
+    cnt[cnt < 12] = 0                                              # experts nobody routes to
+    for my_rank in range(world):
+        off = torch.empty(E, dtype=torch.int32, device=DEV)
+        mbe = torch.empty(max_blocks, dtype=torch.int32, device=DEV)
+        nb = torch.empty(1, dtype=torch.int32, device=DEV)
+        _ext().moe_layout(cnt.to(DEV), world, my_rank, off, mbe, nb, align)
+        r_off, r_mbe, r_total = _layout_ref(cnt, world, my_rank, max_blocks, align)
+        assert off.cpu().tolist() == r_off
+        assert mbe.cpu().tolist() == r_mbe
+        assert int(nb.item()) == r_total
