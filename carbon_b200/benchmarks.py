@@ -146,6 +146,35 @@ def bench_mhc(a):
                       "gemm_tflops": round(flops / (ms - ms_mix) / 1e9, 1), "peak_src": pk["src"]}))
 
 
+def bench_boundary(a):
+    """Fused decode mHC boundary (post-mix + statistics + Sinkhorn coefficients + pre-norm, one launch) at the full
+    width: --decode-tokens tokens x 4 streams x --hidden; cold L2 (flushed) and warm."""
+    from .models.deepseek import make_hc
+    from .ops._ext import ext
+    from .ops.quant import empty_sf
+
+    T, D, dev = a.decode_tokens, a.hidden, torch.device("cuda")
+    hp = make_hc(torch.randn(24, 4 * D) * 0.02, torch.randn(24) * 0.5, torch.rand(3) + 0.5, dev)
+    w = torch.rand(D, device=dev) + 0.5
+    X = torch.randn(T, 4, D, device=dev).to(torch.bfloat16)
+    out = torch.randn(T, D, device=dev).to(torch.bfloat16)
+    post = torch.rand(T, 4, device=dev)
+    comb = torch.softmax(torch.randn(T, 4, 4, device=dev), -1)
+    y = torch.empty(T, D, dtype=torch.bfloat16, device=dev)
+    q = torch.empty(T, D, dtype=torch.float8_e4m3fn, device=dev)
+    sf = empty_sf(T, D, dev)
+    p2, po2, c2 = torch.empty(T, 4, device=dev), torch.empty(T, 4, device=dev), torch.empty(T, 4, 4, device=dev)
+
+    def step():
+        ext().mhc_boundary_small(X, out, post, comb, hp.fn, hp.base, hp.scale, 20, 1e-6, 1e-6, w, y, q, sf, p2, po2,
+                                 c2)
+
+    cold = time_fn(step, iters=20, flush=True)
+    warm = time_fn(step, iters=20, flush=False)
+    print(json.dumps({"bench": "mhc_boundary_decode", "tokens": T, "hidden": D, "us_cold_l2": round(cold * 1e3, 2),
+                      "us_warm_l2": round(warm * 1e3, 2)}))
+
+
 def bench_decode_attn(a):
     from .ops.attention import sparse_mla
 
@@ -265,7 +294,7 @@ def bench_moe(a):
 
 def main(argv=None):
     ap = argparse.ArgumentParser()
-    ap.add_argument("what", choices=["attn", "gemm", "mhc", "decode_attn", "decode_indexer", "moe"])
+    ap.add_argument("what", choices=["attn", "gemm", "mhc", "boundary", "decode_attn", "decode_indexer", "moe"])
     ap.add_argument("--experts", type=int, default=256)
     ap.add_argument("--inter", type=int, default=2048)
     ap.add_argument("--comm", default="fused", choices=["fused", "nccl"])
@@ -285,12 +314,13 @@ def main(argv=None):
     ap.add_argument("--k", type=int, default=7168)
     ap.add_argument("--tokens", type=int, default=16384)
     ap.add_argument("--hidden", type=int, default=7168)
+    ap.add_argument("--decode-tokens", type=int, default=32, help="boundary: decode batch")
     ap.add_argument("--attn-version", type=int, default=0,
                     help="attn: 3 = two Q tiles, 64-key steps, double-buffered S; 2 = two Q tiles, 128-key steps; 1 = one")
     ap.add_argument("--pair", type=int, default=-1, help="gemm: -1 auto, 1 CTA-pair 256x256 tiles, 0 128x128 tiles")
     a = ap.parse_args(argv)
     sys.path.insert(0, ROOT)
-    {"attn": bench_attn, "gemm": bench_gemm, "mhc": bench_mhc, "decode_attn": bench_decode_attn,
+    {"attn": bench_attn, "gemm": bench_gemm, "mhc": bench_mhc, "boundary": bench_boundary, "decode_attn": bench_decode_attn,
      "decode_indexer": bench_decode_indexer, "moe": bench_moe}[a.what](a)
 
 

@@ -63,6 +63,32 @@ CB_DEVICE float warp_sum(float v) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
+// Warp totals of NV per-lane values with NV/2 + NV/4 + ... + 1 (+ the remaining plain steps) shuffles instead of
+// 5 NV: at each butterfly step a lane keeps one half of its values, receives its partner's partial of that half and
+// sends the other.  Afterwards lane l holds the total of value  l >> (5 - log2 NV)  (NV = 8, 16 or 32).
+template <int NV>
+CB_DEVICE float warp_sum_many(float (&v)[NV], int lane) {
+  static_assert(NV == 8 || NV == 16 || NV == 32, "warp_sum_many: NV in {8, 16, 32}");
+  int n = NV;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    if (n > 1) {
+      const int half = n >> 1;
+      const bool up = (lane & off) != 0;
+#pragma unroll
+      for (int i = 0; i < NV / 2; ++i)
+        if (i < half) {
+          const float send = up ? v[i] : v[i + half];
+          const float keep = up ? v[i + half] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+        }
+      n = half;
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], off);
+    }
+  }
+  return v[0];
+}
 CB_DEVICE float warp_max(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));

@@ -124,16 +124,17 @@ static cudaError_t splitk_reduce(const float* part, int splits, int M, int N, in
 }
 
 // Sum of the float4 at p in `splits` consecutive slabs (stride `slab` floats), added in split order; the loads of up
-// to 8 splits are issued before any is used, so a reduction costs one memory latency per 8 splits, not one per split.
+// to U splits are issued before any is used, so a reduction costs one memory latency per U splits, not one per split.
+template <int U = 8>
 CB_DEVICE float4 splits_sum4(const float* __restrict__ p, size_t slab, int splits) {
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int sp0 = 0; sp0 < splits; sp0 += 8) {
-    float4 v[8];
+  for (int sp0 = 0; sp0 < splits; sp0 += U) {
+    float4 v[U];
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < U; ++j)
       if (sp0 + j < splits) v[j] = *reinterpret_cast<const float4*>(p + size_t(sp0 + j) * slab);
 #pragma unroll
-    for (int j = 0; j < 8; ++j)
+    for (int j = 0; j < U; ++j)
       if (sp0 + j < splits) { acc.x += v[j].x; acc.y += v[j].y; acc.z += v[j].z; acc.w += v[j].w; }
   }
   return acc;
@@ -166,8 +167,8 @@ CB_DEVICE void swiglu_reduce_row(const float* __restrict__ part, int splits, int
   float amax = 0.f;
   // gate and up sums of this lane's 4 columns (float4 loads, every split's load in flight before the adds)
   const float* pr = part + size_t(row) * N + 256 * g + 4 * lane;
-  const float4 g4 = splits_sum4(pr, size_t(M) * N, splits);
-  const float4 u4 = splits_sum4(pr + 128, size_t(M) * N, splits);
+  const float4 g4 = splits_sum4<4>(pr, size_t(M) * N, splits);
+  const float4 u4 = splits_sum4<4>(pr + 128, size_t(M) * N, splits);
   const float gs[4] = {g4.x, g4.y, g4.z, g4.w}, us[4] = {u4.x, u4.y, u4.z, u4.w};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -193,7 +194,8 @@ CB_DEVICE void swiglu_reduce_row(const float* __restrict__ part, int splits, int
 // Dense calls (row_valid == nullptr): warps stride over every (row, column group).  Grouped calls (a row_valid map,
 // the used 128-row blocks counted on the device): one CTA per 128-row block; CTAs past the used blocks and padding
 // rows return at once, so a decode call touches only its few routed rows out of the padded capacity.
-__global__ void splitk_reduce_swiglu_kernel(const float* __restrict__ part, int splits, int M, int N, float limit,
+__global__ void __launch_bounds__(512) splitk_reduce_swiglu_kernel(const float* __restrict__ part, int splits, int M,
+                                                                   int N, float limit,
                                             uint8_t* __restrict__ out, int ldo, uint32_t* __restrict__ out_sf,
                                             int sf_row_blocks, const int* __restrict__ row_valid,
                                             const int* __restrict__ n_blocks) {
@@ -315,7 +317,9 @@ cudaError_t gemm_fp8(const void* A, const void* B, const uint32_t* sfa, const ui
       if (e != cudaSuccess) return e;
       // one CTA per 128-row block when a row map is given (grouped call), else warps striding over the rows
       const int grid = row_valid ? ceil_div(M, 128) : min(ceil_div(M * (N / 256), 8), num_sms * 8);
-      cb::launch_k(splitk_reduce_swiglu_kernel, grid, 256, 0, s, work, 1, M, N, swiglu_limit,
+      // 16 warps per row block: a decode block's few rows x 16 column groups are one or two items per warp, so
+      // their loads (partials mostly evicted from L2 by the weight stream) are in flight together
+      cb::launch_k(splitk_reduce_swiglu_kernel, grid, row_valid ? 512 : 256, 0, s, work, 1, M, N, swiglu_limit,
                                                                      reinterpret_cast<uint8_t*>(out), ldo, out_sf,
                                                                      ceil_div(M, 128), row_valid, num_m_blocks_dev);
       return cudaGetLastError();

@@ -864,7 +864,8 @@ __global__ void __cluster_dims__(kBndCluster, 1, 1) __launch_bounds__(kBndThread
   }
   cb::pdl_entry();
   __shared__ float xs_sm[TT][4][kBndCols * 8];                // the new streams of this CTA's columns
-  __shared__ float part[kBndWarps][TT * 8];                   // per-warp partials of one 8-row group
+  __shared__ float part[kBndWarps][TT * 8];                   // per-warp partials (phase D)
+  __shared__ float pall[kBndWarps][TT * (kBndStats + 1)];     // per-warp totals of the statistics, then Σx²
   __shared__ float red[TT][kBndStats + 1];                    // this CTA's stats partials + Σx² (read cluster-wide)
   __shared__ float tot[TT][kBndStats + 1];
   __shared__ float coef[TT][24];                              // pre[4], post[4], comb[16]
@@ -952,33 +953,33 @@ __global__ void __cluster_dims__(kBndCluster, 1, 1) __launch_bounds__(kBndThread
           for (int j = 0; j < 8; ++j) acc[i][rr] += xg[i][j] * f[j];
       }
     }
+    {
+      // warp totals of the TT x 8 partials in one butterfly (TT*8 - 1 + ... shuffles instead of 5 TT*8)
+      constexpr int NV = TT * 8, SH = NV == 8 ? 2 : NV == 16 ? 1 : 0;
+      float flat[NV];
 #pragma unroll
-    for (int i = 0; i < TT; ++i)
+      for (int i = 0; i < TT; ++i)
 #pragma unroll
-      for (int rr = 0; rr < 8; ++rr) {
-        const float v = warp_sum(acc[i][rr]);
-        if (lane == 0) part[wid][i * 8 + rr] = v;
+        for (int rr = 0; rr < 8; ++rr) flat[i * 8 + rr] = acc[i][rr];
+      const float v = warp_sum_many<NV>(flat, lane);
+      if ((lane & ((1 << SH) - 1)) == 0) {
+        const int idx = lane >> SH;                          // = token * 8 + row within the group
+        pall[wid][(idx >> 3) * kBndStats + r0 + (idx & 7)] = v;
       }
-    __syncthreads();
-    if (threadIdx.x < TT * 8) {
-      float v = 0.f;
-#pragma unroll
-      for (int ww = 0; ww < kBndWarps; ++ww) v += part[ww][threadIdx.x];
-      red[threadIdx.x / 8][r0 + threadIdx.x % 8] = v;
     }
-    __syncthreads();
   }
 #pragma unroll
   for (int i = 0; i < TT; ++i) {
     const float v = warp_sum(ss[i]);
-    if (lane == 0) part[wid][i] = v;
+    if (lane == 0) pall[wid][TT * kBndStats + i] = v;
   }
-  __syncthreads();
-  if (threadIdx.x < TT) {
+  __syncthreads();                                           // one barrier for all 48 statistics and Σx²
+  for (int e = threadIdx.x; e < TT * (kBndStats + 1); e += kBndThreads) {
     float v = 0.f;
 #pragma unroll
-    for (int ww = 0; ww < kBndWarps; ++ww) v += part[ww][threadIdx.x];
-    red[threadIdx.x][kBndStats] = v;
+    for (int ww = 0; ww < kBndWarps; ++ww) v += pall[ww][e];
+    if (e < TT * kBndStats) red[e / kBndStats][e % kBndStats] = v;
+    else red[e - TT * kBndStats][kBndStats] = v;
   }
   cluster_sync();                                            // every CTA's partials are visible cluster-wide
   for (int e = threadIdx.x; e < TT * (kBndStats + 1); e += kBndThreads) {
