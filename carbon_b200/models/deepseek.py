@@ -159,6 +159,7 @@ class DeepseekModel:
         self.owner_kv = False      # only a request's home rank caches its KV (no all-gather of the new rows)
         self._side = None          # side stream of the shared expert
         self._dsa = {}
+        self._early_sel: Dict[int, Pending] = {}   # decode DSA selections started before the query projections
         cfg.validate()
         if cfg.swa_window and cfg.attn_kind != "latent_mqa":
             raise NotImplementedError("swa_window is served by the latent-MQA attention path only")
@@ -553,6 +554,8 @@ class DeepseekModel:
             cache.write_latent(i, out_loc, latent_c)
             if idx_k is not None:
                 cache.write_index_k(i, out_loc, idx_k)
+        if idx_l is not None and self._selection_early(i, fb, dp):
+            self._early_sel[i] = self._start_selection(i, fb, cache, idx_l)
         T = q_lat.shape[0]
         dq = cfg.qk_head_dim
         with region("attn.q_proj"):
@@ -593,13 +596,22 @@ class DeepseekModel:
     def indexer_qkw(self, i, h, q_lat, pos, q_lat_q=None):
         cfg, L = self.cfg, self.layers[i]
         T, Hi, Di, dr = h.shape[0], cfg.index_n_heads, cfg.index_head_dim, cfg.qk_rope_head_dim
-        q = L.idx_wq(q_lat, xq=q_lat_q).view(T, Hi, Di)
-        if not self.on_gpu:
-            q = q.clone()
-        C.rope_(q, 0, dr, self.cos_sin, pos)
         if self.on_gpu:
             from ..ops._ext import ext
 
+            # decode-size batches: the query projection (from q_lat) runs on the side stream while the key /
+            # head-weight projection (from h) runs here, joined before returning (prefill GEMMs fill the GPU alone)
+            cur = torch.cuda.current_stream()
+            side = self._index_stream() if T <= 1024 else cur
+            if side is not cur:
+                side.wait_stream(cur)
+                for t_ in (q_lat, pos) + (tuple(q_lat_q) if q_lat_q is not None else ()):
+                    t_.record_stream(side)
+            with torch.cuda.stream(side):
+                q = L.idx_wq(q_lat, xq=q_lat_q).view(T, Hi, Di)
+                C.rope_(q, 0, dr, self.cos_sin, pos)
+            if side is not cur:
+                q.record_stream(cur)
             kw = L.idx_wkp(h, out_dtype=torch.float32)                               # [T, Di + Hi]
             k = torch.empty(T, Di, dtype=torch.bfloat16, device=h.device)
             w = torch.empty(T, Hi, dtype=torch.float32, device=h.device)
@@ -608,7 +620,11 @@ class DeepseekModel:
                                   self.cos_sin, pos.to(torch.int32).contiguous(), dr, (Hi ** -0.5) * (Di ** -0.5),
                                   k, w)
             k = k.view(T, 1, Di)
+            if side is not cur:
+                cur.wait_stream(side)
         else:
+            q = L.idx_wq(q_lat, xq=q_lat_q).view(T, Hi, Di).clone()
+            C.rope_(q, 0, dr, self.cos_sin, pos)
             k = F.layer_norm(L.idx_wk(h).float(), (Di,), L.idx_kn_w, L.idx_kn_b, 1e-6).to(self.act_dtype)
             w = (L.idx_wp(h, out_dtype=torch.float32) * (Hi ** -0.5) * (Di ** -0.5)).float()
             k = k.view(T, 1, Di)
@@ -794,19 +810,15 @@ class DeepseekModel:
         else:
             idx = fb.key_slots[lo:hi] if local else fb.key_slots
         pending = None
+        early = self._early_sel.pop(i, None)
         if sel is None and src is not None and int(fb.key_slots.shape[1]) > cfg.index_topk:
             if src == i:
                 qi, _, wi = idx_l
                 ks, nk = fb.key_slots[lo:hi].contiguous(), fb.n_keys[lo:hi].contiguous()
-                if self.on_gpu and local:
-                    # the DSA selection runs on a side stream, overlapping the query absorption below (the
-                    # reference's decode index streams)
-                    side = self._index_stream()
-                    side.wait_stream(torch.cuda.current_stream())
-                    for t_ in (qi, wi, ks, nk):
-                        t_.record_stream(side)
-                    with torch.cuda.stream(side), region("attn.indexer_topk"):
-                        pending = Pending(A.indexer_topk(qi, wi, cache.index_k[i], ks, nk, cfg.index_topk), side)
+                if early is not None:
+                    pending = early                 # started on the side stream right after the key-cache write
+                elif self.on_gpu and (local or pc.world == 1):
+                    pending = self._start_selection(i, fb, cache, idx_l)
                 else:
                     with region("attn.indexer_topk"):
                         sel = A.indexer_topk(qi, wi, cache.index_k[i], ks, nk, cfg.index_topk)
@@ -837,6 +849,32 @@ class DeepseekModel:
                 o_lat = A.sparse_mla(qf, cache.latent[i], idx.contiguous(), cfg.softmax_scale, r, sink=L.sink)
         with region("attn.absorb_o"):
             return head_bmm(o_lat, L.w_uv), False                                    # [T, Hl, dv]
+
+    def _selection_early(self, i: int, fb, dp: bool) -> bool:
+        """Whether this decode layer's DSA selection can start on the side stream as soon as the new index keys are
+        in the cache (before the query projections): the GPU path of an index-source MLA layer whose core reads
+        only this rank's queries (token-parallel TP, data-parallel attention, or one rank)."""
+        cfg, pc = self.cfg, self.pctx
+        if not self.on_gpu or fb.is_prefill or cfg.attn_kind != "mla" or cfg.index_source(i) != i:
+            return False
+        if int(fb.key_slots.shape[1]) <= cfg.index_topk:
+            return False
+        swap = not dp and pc.world > 1 and hasattr(pc, "heads_to_tokens")
+        return dp or swap or pc.world == 1
+
+    def _start_selection(self, i: int, fb, cache, idx_l) -> Pending:
+        """DSA top-k of this rank's decode queries on the side stream (the reference's decode index streams): it
+        overlaps the query projection and absorption on the main stream until ``Pending.get()``."""
+        cfg = self.cfg
+        lo, hi = self.pctx.local
+        qi, _, wi = idx_l
+        ks, nk = fb.key_slots[lo:hi].contiguous(), fb.n_keys[lo:hi].contiguous()
+        side = self._index_stream()
+        side.wait_stream(torch.cuda.current_stream())
+        for t_ in (qi, wi, ks, nk):
+            t_.record_stream(side)
+        with torch.cuda.stream(side), region("attn.indexer_topk"):
+            return Pending(A.indexer_topk(qi, wi, cache.index_k[i], ks, nk, cfg.index_topk), side)
 
     def _index_stream(self):
         if getattr(self, "_idx_side", None) is None:
@@ -926,6 +964,7 @@ class DeepseekModel:
         T_all = fb.ids.shape[0]
         self.pctx.set_bounds(fb.bounds if fb.bounds is not None else [0, T_all])
         self._dsa = {}                 # DSA selections of this forward's index-source layers
+        self._early_sel = {}
         lo, hi = self.pctx.local
         self._tok_local = fb.ids[lo:hi]    # this rank's token ids (multimodal router bias, Engram image skip)
         with region("embed"):
