@@ -126,14 +126,6 @@ class RefModel:
         self.forced_routing = None   # {layer: ids [T, k]}: use these expert choices instead of the router's top-k
         self.forced_dsa = None       # {layer: positions [T, topk] (-1 pad)}: use this DSA selection instead
         self._dsa = {}               # DSA selection of each index-source layer in the current forward
-        self.act_fp8 = False         # round every fp8 GEMM's input to e4m3 (1x128 UE8M0) as the GPU path does
-
-    def _q(self, x: torch.Tensor) -> torch.Tensor:
-        """Input of a GEMM that the GPU runs in fp8 (inner dim a multiple of 128): with ``act_fp8`` rounded to e4m3
-        with one power-of-two scale per 128 elements, exactly the GPU's activation quantiser; else unchanged."""
-        if not self.act_fp8 or x.shape[-1] % 128:
-            return x
-        return ops.fake_quant_fp8_rows(x)
 
     # -- sublayers -------------------------------------------------------------------------------------------------
     def attention(self, i: int, h: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
@@ -142,14 +134,14 @@ class RefModel:
         T, H = h.shape[0], cfg.n_heads
         dr, r, dq = cfg.qk_rope_head_dim, cfg.kv_lora_rank, cfg.qk_head_dim
         if cfg.q_lora_rank > 0:
-            q_lat = ops.rms_norm(self._q(h) @ w[L + "wq_a.weight"].t(), w[L + "q_norm.weight"], cfg.rms_eps)
-            q = (self._q(q_lat) @ w[L + "wq_b.weight"].t()).view(T, H, dq)
+            q_lat = ops.rms_norm(h @ w[L + "wq_a.weight"].t(), w[L + "q_norm.weight"], cfg.rms_eps)
+            q = (q_lat @ w[L + "wq_b.weight"].t()).view(T, H, dq)
         else:
             q_lat = h
-            q = (self._q(h) @ w[L + "wq.weight"].t()).view(T, H, dq)
+            q = (h @ w[L + "wq.weight"].t()).view(T, H, dq)
         dn = dq - dr                                  # non-RoPE part of q
         qf = torch.cat([q[..., :dn], ops.apply_rope(q[..., dn:], pos, cfg.rope)], dim=-1)
-        kv = self._q(h) @ w[L + "wkv_a.weight"].t()
+        kv = h @ w[L + "wkv_a.weight"].t()
         if cfg.attn_kind == "latent_mqa":
             # one shared head: the normalised latent, RoPE on its last dr dims; value = the same row
             kv_c = ops.rms_norm(kv, w[L + "kv_norm.weight"], cfg.rms_eps)
@@ -160,7 +152,7 @@ class RefModel:
             dv = cfg.v_head_dim
             kv_c = ops.rms_norm(kv[:, :r], w[L + "kv_norm.weight"], cfg.rms_eps)
             k_pe = ops.apply_rope(kv[:, None, r:], pos, cfg.rope)         # [T,1,dr]
-            kvb = (self._q(kv_c) @ w[L + "wkv_b.weight"].t()).view(T, H, dn + dv)
+            kvb = (kv_c @ w[L + "wkv_b.weight"].t()).view(T, H, dn + dv)
             k = torch.cat([kvb[..., :dn], k_pe.expand(T, H, dr)], dim=-1)
             v = kvb[..., dn:]
         W = cfg.swa_window
@@ -200,11 +192,11 @@ class RefModel:
         L = f"layers.{i}.attn."
         T, H = o.shape[0], o.shape[1]
         if not cfg.o_groups:
-            return self._q(o.reshape(T, o.shape[1] * o.shape[2])) @ w[L + "wo.weight"].t()
+            return o.reshape(T, o.shape[1] * o.shape[2]) @ w[L + "wo.weight"].t()
         G = cfg.o_groups
         og = o.reshape(T, G, -1)                                                # [T, G, (H/G)*dvh]
         z = torch.einsum("tgk,gnk->tgn", og, w[L + "wo_a.weight"])              # [T, G, o_lora]
-        return self._q(z.reshape(T, z.shape[1] * z.shape[2])) @ w[L + "wo_b.weight"].t()
+        return z.reshape(T, z.shape[1] * z.shape[2]) @ w[L + "wo_b.weight"].t()
 
     def indexer_logits(self, i: int, h: torch.Tensor, q_lat: torch.Tensor, pos: torch.Tensor) -> torch.Tensor:
         q, k, wt = self.indexer_qkw(i, h, q_lat, pos)
@@ -229,8 +221,7 @@ class RefModel:
         cfg, w = self.cfg, self.w
         L = f"layers.{i}.ffn."
         if not cfg.is_moe_layer(i):
-            hq = self._q(h)
-            return self._q(ops.swiglu(hq @ w[L + "w1"].t(), hq @ w[L + "w3"].t(), cfg.swiglu_limit)) @ w[L + "w2"].t()
+            return ops.swiglu(h @ w[L + "w1"].t(), h @ w[L + "w3"].t(), cfg.swiglu_limit) @ w[L + "w2"].t()
         logits = h @ w[L + "gate.weight"].t()
         bias = w[L + "gate.bias"]
         if cfg.image_token_id >= 0:             # image tokens rank with their own bias
@@ -251,14 +242,13 @@ class RefModel:
             rows, slot = torch.nonzero(ids == e, as_tuple=True)
             if rows.numel() == 0:
                 continue
-            x = self._q(h[rows])
+            x = h[rows]
             y = ops.swiglu(x @ w[L + "experts.w1"][e].t(), x @ w[L + "experts.w3"][e].t(), cfg.swiglu_limit)
-            y = self._q(y) @ w[L + "experts.w2"][e].t()
+            y = y @ w[L + "experts.w2"][e].t()
             out.index_add_(0, rows, y * wts[rows, slot][:, None])
         if cfg.n_shared_experts > 0:
-            hq = self._q(h)
-            out = out + self._q(ops.swiglu(hq @ w[L + "shared.w1"].t(), hq @ w[L + "shared.w3"].t(),
-                                           cfg.swiglu_limit)) @ w[L + "shared.w2"].t()
+            out = out + ops.swiglu(h @ w[L + "shared.w1"].t(), h @ w[L + "shared.w3"].t(),
+                                   cfg.swiglu_limit) @ w[L + "shared.w2"].t()
         return out
 
     def hc_sublayer(self, X, prefix: str, norm_w: torch.Tensor, fn_apply) -> torch.Tensor:

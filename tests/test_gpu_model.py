@@ -1,8 +1,10 @@
 """GPU engine (fp8 weights/activations, bf16 elsewhere, sm_100a kernels) against the CPU fp32 oracle.
 
 fp8 noise compounds through the layers and flips some router choices, so the whole-model comparison uses the
-oracle with the same fp8-rounded weights and a loose bound; the tight checks are the isolated MoE layer with fixed
-routing and the prefill-vs-decode consistency of the GPU engine itself.
+oracle with the same fp8-rounded weights, the GPU's expert choices, and a bound of 0.12 on the relative error of the
+last logits: on B200 these cases measure 0.065-0.085.  An oracle that also rounded every fp8 GEMM input to e4m3
+exactly as the GPU does measured the same 0.065-0.096, so the remaining gap is not activation quantisation.  The
+tight checks are the isolated MoE layer with fixed routing and the prefill-vs-decode consistency of the GPU engine.
 """
 import pytest
 import torch
@@ -76,7 +78,7 @@ def test_small_model_vs_oracle(plen):
     # the oracle follows the GPU's expert choices: a near-tie in the router is not a numerics error
     ref.forced_routing = {int(k.split(".")[0]): v.long() for k, v in eng.model.trace if k.endswith("router_ids")}
     exp = ref.forward(prompt)[-1]
-    assert _rel(got, exp) < 0.15, _rel(got, exp)
+    assert _rel(got, exp) < 0.12, _rel(got, exp)
     assert torch.corrcoef(torch.stack([got, exp]))[0, 1] > 0.98
 
 
@@ -145,7 +147,7 @@ def test_v4_latent_mqa_model_vs_oracle(plen):
     ref.forced_routing = {int(k.split(".")[0]): v.long() for k, v in eng.model.trace if k.endswith("router_ids")}
     ref.forced_dsa = {int(k.split(".")[0]): v.long() for k, v in eng.model.trace if k.endswith("dsa_pos")}
     exp = ref.forward(prompt)[-1]
-    assert _rel(got, exp) < 0.15, _rel(got, exp)
+    assert _rel(got, exp) < 0.12, _rel(got, exp)
     assert torch.corrcoef(torch.stack([got, exp]))[0, 1] > 0.98
 
 
@@ -242,7 +244,7 @@ def test_v4_late_replay_vs_oracle():
     ref.forced_routing = {int(k.split(".")[0]): v.long() for k, v in eng.model.trace if k.endswith("router_ids")}
     ref.forced_dsa = {int(k.split(".")[0]): v.long() for k, v in eng.model.trace if k.endswith("dsa_pos")}
     exp = ref.forward(prompt)[-1]
-    assert _rel(got, exp) < 0.15, _rel(got, exp)
+    assert _rel(got, exp) < 0.12, _rel(got, exp)
     assert torch.corrcoef(torch.stack([got, exp]))[0, 1] > 0.98
 
 
@@ -262,7 +264,7 @@ def test_fp8_indexer_model_vs_oracle():
     got = eng.prefill([r])[0].float().cpu()
     ref.forced_routing = {int(k.split(".")[0]): v.long() for k, v in eng.model.trace if k.endswith("router_ids")}
     exp = ref.forward(prompt)[-1]
-    assert _rel(got, exp) < 0.15, _rel(got, exp)
+    assert _rel(got, exp) < 0.12, _rel(got, exp)
     # GPU self-consistency with real pruning (top-128): fp8 prefill selection vs bf16 decode on the same values
     cfg = _cfg().replace(index_fp8=True, index_topk=128)
     eng = Engine(cfg, device="cuda", source=WeightSource(cfg, state=w), num_pages=32, page_size=64)
@@ -289,7 +291,7 @@ def test_plain_residual_model_vs_oracle():
     got = eng.prefill([r])[0].float().cpu()
     ref.forced_routing = {int(k.split(".")[0]): v.long() for k, v in eng.model.trace if k.endswith("router_ids")}
     exp = ref.forward(prompt)[-1]
-    assert _rel(got, exp) < 0.15, _rel(got, exp)
+    assert _rel(got, exp) < 0.12, _rel(got, exp)
     eng.model.trace = None
     r1 = eng.add_request(prompt[:-1].tolist())
     eng.prefill([r1])
