@@ -1,5 +1,5 @@
-"""Op-level benchmarks (attention, mHC + GEMM, MoE, GEMM, decode attention), timed on the device with CUDA events and reported against the
-measured roofline (``MEASURED_PEAKS.json`` when present: ``bf16_tflops``, ``hbm_gbs``).
+"""Op-level benchmarks (attention, mHC + GEMM, decode mHC boundary, MoE, GEMM, decode attention and indexer), timed
+on the device with CUDA events and reported against the measured roofline (``MEASURED_PEAKS.json`` when present: ``bf16_tflops``, ``hbm_gbs``).
 
     python -m carbon_b200.benchmarks attn  [--batch 4 --seq 8192 --heads 128 --dsa]   # config 2
     python -m carbon_b200.benchmarks mhc   [--tokens 16384 --hidden 7168 --n 24576]   # config 3
@@ -320,7 +320,8 @@ def main(argv=None):
     ap.add_argument("--pair", type=int, default=-1, help="gemm: -1 auto, 1 CTA-pair 256x256 tiles, 0 128x128 tiles")
     a = ap.parse_args(argv)
     sys.path.insert(0, ROOT)
-    {"attn": bench_attn, "gemm": bench_gemm, "mhc": bench_mhc, "boundary": bench_boundary, "decode_attn": bench_decode_attn,
+    {"attn": bench_attn, "gemm": bench_gemm, "mhc": bench_mhc, "boundary": bench_boundary,
+     "decode_attn": bench_decode_attn,
      "decode_indexer": bench_decode_indexer, "moe": bench_moe}[a.what](a)
 
 

@@ -292,9 +292,9 @@ cudaError_t moe_layout(const int* cnt, int world, int E, int my_rank, int max_bl
 constexpr int kDispatchCols = 1024;      // columns of a token row per dispatch CTA (a multiple of 512)
 constexpr int kSplitRowsBelow = 1024;    // token counts below this split each row over several CTAs
 
-// Dispatch: one CTA per local token (or, for decode batches, per 1024 columns of it); the row is quantised once (1x128 UE8M0 blocks), then written to
-// each selected expert's owner at row  my_off[e] + pair_rank.  Destination rows are stored in pos_out [T, k]
-// (row index inside the owner's buffer, -1 if it did not fit) for a pull combine; with rinfo_ptrs the owner also
+// Dispatch: one CTA per local token (for decode batches, one per 1024 columns of it); the row is quantised once
+// (1x128 UE8M0 blocks), then written to each selected expert's owner at row  my_off[e] + pair_rank.  Destination
+// rows are stored in pos_out [T, k] (row index inside the owner's buffer, -1 if it did not fit) for a pull combine; with rinfo_ptrs the owner also
 // learns where each received row goes back to: rinfo_owner[row] = (my_rank << 24) | (t * k + j), the slot of this
 // token's j-th expert in this rank's combine buffer (push combine from the owner's GEMM epilogue).
 // recv_ptrs[r]: fp8 rows [cap, D]; sf_ptrs[r]: SF tiles of those rows (row blocks = cap/128).
