@@ -1145,8 +1145,8 @@ def head_bmm(x: torch.Tensor, w: torch.Tensor, tail: int = 0, out_dtype=torch.bf
 
 def _head_bmm_direct(x: torch.Tensor, w: torch.Tensor, tail: int, out_dtype) -> bool:
     """Whether the decode-batch kernel takes this per-head matmul: at most 256 tokens, 128-multiple N, 64-multiple K,
-    8-multiple tail, bf16 operands with 16-byte aligned rows (its tensor maps), bf16 / fp16 output.  CARBON_HEAD_BMM=0 turns it off
-    (the grouped-GEMM path over head-major copies then runs)."""
+    8-multiple tail, bf16 operands with 16-byte aligned rows (its tensor maps), bf16 / fp16 output.
+    CARBON_HEAD_BMM=0 turns it off (the grouped-GEMM path over head-major copies then runs)."""
     T, H, Kx = x.shape
     N, K = w.shape[1], w.shape[2]
     return (_HEAD_BMM_ON and 0 < T <= 256 and N % 128 == 0 and K % 64 == 0 and x.dtype == torch.bfloat16
