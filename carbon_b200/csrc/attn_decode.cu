@@ -204,11 +204,11 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
       for (int la = 0; la < nac; ++la) tma_load_3d(sQ + la * Q_ATOM, &tm_q, q_full, atom_of(hh, la) * 64, 0, t);
     }
     // KT == 32: one key per lane; the next tile's slot is loaded while this tile's gathers are issued
-    int next = k_begin + lane < k_end ? __ldg(idx_t + k_begin + lane) : 0;
+    int next = k_begin + lane < k_end ? idx_t[k_begin + lane] : 0;
     for (int j = 0; j < n_tiles; ++j) {
       int slot = next;
       const int nk = k_begin + (j + 1) * KT + lane;
-      next = (j + 1 < n_tiles && nk < k_end) ? __ldg(idx_t + nk) : 0;
+      next = (j + 1 < n_tiles && nk < k_end) ? idx_t[nk] : 0;
       if (slot < 0) slot = 0;                                  // masked in softmax; keep the address valid
       const int s = F8 ? j % F8_SLOTS : j % STAGES;
       uint64_t* full = F8 ? &st_full[s] : &kv_full[s];
@@ -345,12 +345,12 @@ __global__ void __launch_bounds__(256, 1) sparse_mla_kernel(const __grid_constan
     bool ok = true;
     // validity of a tile's keys (one per lane): the slot of the next tile is loaded one tile ahead, so its global
     // load latency stays off the per-tile chain
-    int next_slot = k_begin + lane < k_end ? __ldg(idx_t + k_begin + lane) : -1;
+    int next_slot = k_begin + lane < k_end ? idx_t[k_begin + lane] : -1;
     for (int j = 0; j < n_tiles; ++j) {
       const int b = j & 1;
       const int my_slot = next_slot;
       const int nk = k_begin + (j + 1) * KT + lane;
-      next_slot = nk < k_end ? __ldg(idx_t + nk) : -1;
+      next_slot = nk < k_end ? idx_t[nk] : -1;
       if (!mbar_wait(&s_full[b], (j >> 1) & 1)) { fail(kErrTimeoutTmem); ok = false; break; }
       if (row == 0) CB_ATTN_TRACE(4, j);
       tc_fence_after();

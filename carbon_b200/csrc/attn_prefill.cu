@@ -525,7 +525,7 @@ __global__ void __launch_bounds__(384, 1) attn_prefill2_kernel(const __grid_cons
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const int wi = ((jj * BN) >> 5) + c;
-        w[c] = wi < p.mask_words ? __ldg(p.mask + size_t(tok) * p.mask_words + wi) : 0u;
+        w[c] = wi < p.mask_words ? p.mask[size_t(tok) * p.mask_words + wi] : 0u;
       }
     };
     uint32_t mwn[4] = {0xffffffffu, 0xffffffffu, 0xffffffffu, 0xffffffffu};
@@ -817,8 +817,8 @@ __global__ void __launch_bounds__(384, 1) attn_prefill3_kernel(const __grid_cons
     const bool use_mask = p.mask != nullptr && qi < seq_len;
     auto load_mask = [&](int jj, uint32_t& w0, uint32_t& w1) {
       const int wi = (jj * BN) >> 5;
-      w0 = wi < p.mask_words ? __ldg(p.mask + size_t(tok) * p.mask_words + wi) : 0u;
-      w1 = wi + 1 < p.mask_words ? __ldg(p.mask + size_t(tok) * p.mask_words + wi + 1) : 0u;
+      w0 = wi < p.mask_words ? p.mask[size_t(tok) * p.mask_words + wi] : 0u;
+      w1 = wi + 1 < p.mask_words ? p.mask[size_t(tok) * p.mask_words + wi + 1] : 0u;
     };
     uint32_t mwn0 = 0xffffffffu, mwn1 = 0xffffffffu;
     if (use_mask && nkt > 0) load_mask(0, mwn0, mwn1);

@@ -515,7 +515,7 @@ __global__ void __launch_bounds__(PairCfg<KIND, PAIR, EPI>::kThreads, 1)
             float wv[32];
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-              const float4 x = (i < 4 || two) ? __ldg(w4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+              const float4 x = (i < 4 || two) ? w4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
               wv[4 * i] = x.x; wv[4 * i + 1] = x.y; wv[4 * i + 2] = x.z; wv[4 * i + 3] = x.w;
             }
             tmem_ld_wait();

@@ -108,7 +108,7 @@ __global__ void __launch_bounds__(192) indexer_decode_kernel(const __grid_consta
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int key = (tile0 + j) * KT + lane * 4 + i;
-        const int slot = (j < mma_tiles && key < n) ? __ldg(slots_t + key) : 0;
+        const int slot = (j < mma_tiles && key < n) ? slots_t[key] : 0;
         r[i] = slot < 0 ? 0 : slot;                     // masked in the epilogue; keep the address valid
       }
     };
@@ -173,7 +173,7 @@ __global__ void __launch_bounds__(192) indexer_decode_kernel(const __grid_consta
       tc_fence_before();
       mbar_arrive(&acc_empty[b]);
       const int key = (tile0 + j) * KT + row;
-      if (key < p.Lmax) out_t[key] = (key < n && __ldg(slots_t + key) >= 0) ? acc : -INFINITY;
+      if (key < p.Lmax) out_t[key] = (key < n && slots_t[key] >= 0) ? acc : -INFINITY;
     }
     // keys of this CTA's tiles that are all at or beyond n
     for (int key = (tile0 + mma_tiles) * KT + row; key < min(tile1 * KT, p.Lmax); key += KT) out_t[key] = -INFINITY;
