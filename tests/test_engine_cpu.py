@@ -97,3 +97,21 @@ def test_chunked_prefill_matches_oracle(variant):
             cur = int(torch.argmax(lg))
             got.append(cur)
         assert got == toks[:4]
+
+
+def test_head_bmm_decode_kernel_eligibility():
+    """The decode shapes of the absorbed MLA take the swap-AB per-head kernel (query absorption with its RoPE tail,
+    value un-absorption, V4's grouped wo_a); shapes its tensor maps cannot serve fall back to the grouped GEMM."""
+    from carbon_b200.models.deepseek import _head_bmm_direct
+
+    bf = torch.bfloat16
+    q = torch.zeros(32, 128, 192, dtype=bf)
+    w_uk = torch.zeros(128, 512, 128, dtype=bf)
+    assert _head_bmm_direct(q, w_uk, 64, torch.float16)
+    assert _head_bmm_direct(torch.zeros(32, 128, 512, dtype=bf), torch.zeros(128, 128, 512, dtype=bf), 0, bf)
+    assert _head_bmm_direct(torch.zeros(256, 8, 512, dtype=bf), torch.zeros(8, 1024, 512, dtype=bf), 0, bf)
+    assert not _head_bmm_direct(torch.zeros(257, 128, 192, dtype=bf), w_uk, 64, bf)        # more than 256 tokens
+    assert not _head_bmm_direct(q, torch.zeros(128, 500, 128, dtype=bf), 64, bf)           # N not a multiple of 128
+    assert not _head_bmm_direct(q.float(), w_uk, 64, bf)                                   # fp32 operand
+    assert not _head_bmm_direct(q[:, :, 1:], w_uk, 60, bf)                                 # unaligned rows / tail
+    assert not _head_bmm_direct(q, w_uk, 64, torch.float32)                                # fp32 output
